@@ -1,0 +1,331 @@
+"""Benchmark of the needle B200 batched quantized decode path.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload NAME]
+
+Prints ONE JSON line on rank 0.  For N > 1 launch it with torchrun (one rank
+per GPU, NCCL only for the barrier and the max-over-ranks timing; the decode
+path itself has no collective).  `--impl reference` times the CPU restatement
+of the reference algorithm (the oracle) on the host cores instead.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import numpy as np  # noqa: E402
+
+import __graft_entry__ as entry  # noqa: E402
+
+PEAKS_PATH = os.path.join(ROOT, "MEASURED_PEAKS.json")
+FALLBACK_HBM_GBS = 6650.0
+
+
+def hbm_peak():
+    try:
+        with open(PEAKS_PATH) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+# --------------------------------------------------------------- clocks --
+class ClockSampler:
+    """Samples nvidia-smi clocks/throttle reasons while the timed region runs."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index):
+        self.device_index = device_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits", "-lms", "100",
+                 "-i", str(self.device_index)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._drain, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _drain(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ----------------------------------------------------------- distributed --
+def dist_setup(n_gpus):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(value, world):
+    if world == 1:
+        return value
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ------------------------------------------------------------ workloads --
+class GemvWorkload:
+    """Config 1: the int8 linear [M,512] x [2048,512]^T with per-32-group fp16
+    scales.  One step = the linear over `copies` distinct weight sets in one
+    launch (weights cycled so they stream from HBM, as the reference's
+    kernel bench cycles weight buffers)."""
+
+    name = "cfg1_int8_linear"
+
+    def __init__(self, m=16, n=2048, k=512, copies=192):
+        self.m, self.n, self.k, self.copies = m, n, k, copies
+        self.unit_bytes = n * k + n * (k // 32) * 2 + m * k + m * 4 + m * n * 4
+
+    def setup(self, device):
+        import torch
+
+        self.ops = __import__("needle_cs_b200.ops", fromlist=["ops"])
+        ops = self.ops
+        m, n, k, c = self.m, self.n, self.k, self.copies
+        self.w = torch.empty((c, n, k), dtype=torch.int8, device=device)
+        self.sw = torch.empty((c, n, k // 32), dtype=torch.int16, device=device)
+        ops.synth_int8_device(0, 2, self.w)
+        ops.synth_uniform_f16_device(0, 3, self.sw, 0.001, 0.02)
+        self.x_host = torch.from_numpy(ops.synth_normal_f32(0, 1, m * k).reshape(m, k)).pin_memory()
+        self.x = self.x_host.to(device)
+        self.q, self.sa = ops.quantize_rows(self.x)
+        self.y = torch.empty((c, m, n), dtype=torch.float32, device=device)
+        self.y_host = torch.empty((m, n), dtype=torch.float32).pin_memory()
+        self.x_dev = torch.empty_like(self.x)
+        self.q1 = torch.empty_like(self.q)
+        self.sa1 = torch.empty_like(self.sa)
+        self.y1 = torch.empty((m, n), dtype=torch.float32, device=device)
+        torch.cuda.synchronize()
+
+    def step(self):
+        self.ops.matmul_i8g32_batched(self.q, self.sa, self.w, self.sw, self.y)
+        return 1  # kernel launches
+
+    def units_per_step(self):
+        return self.copies
+
+    def bytes_per_step(self):
+        return self.copies * self.unit_bytes
+
+    def e2e_step(self):
+        """Public-API call with host buffers: H2D of x, quantize, linear, D2H of y."""
+        self.x_dev.copy_(self.x_host, non_blocking=True)
+        self.ops.quantize_rows(self.x_dev, self.q1, self.sa1)
+        self.ops.matmul_i8g32(self.q1, self.sa1, self.w[0], self.sw[0], y=self.y1)
+        self.y_host.copy_(self.y1, non_blocking=True)
+        return 2, self.x_host.numel() * 4, self.y_host.numel() * 4
+
+    def describe(self):
+        return {"workload": self.name, "m": self.m, "n": self.n, "k": self.k, "weight_copies": self.copies,
+                "group": 32, "l2": "inputs exceed L2 (weights cycled over %d MiB)" % (self.copies * self.n * self.k >> 20)}
+
+    # CPU baseline on a bounded sample: the oracle (scalar restatement).
+    def cpu_sample(self, oracle, budget_s=10.0):
+        ops = self.ops
+        m, n, k = self.m, self.n, self.k
+        x = ops.synth_normal_f32(0, 1, m * k).reshape(m, k)
+        w = ops.synth_int8(0, 2, n * k).reshape(n, k)
+        sw = ops.synth_uniform_f16(0, 3, n * (k // 32), 0.001, 0.02).reshape(n, k // 32)
+        q, sa = oracle.quantize_rows(x)
+        calls, t0 = 0, time.perf_counter()
+        while True:
+            oracle.matmul_i8g32(q, sa, w, sw)
+            calls += 1
+            dt = time.perf_counter() - t0
+            if dt >= budget_s or calls >= 200:
+                break
+        return calls * self.unit_bytes / dt / 1e9, f"{calls} calls of the M={m} linear, 1 weight set (L2/LLC-warm)"
+
+
+WORKLOADS = {"cfg1": GemvWorkload}
+
+
+def run_reference(args, rank, world):
+    """CPU restatement of the reference algorithm on the host cores."""
+    if rank != 0:
+        return
+    oracle = entry.load_oracle()
+    entry.load_package()
+    wl = WORKLOADS[args.workload]()
+    wl.ops = __import__("needle_cs_b200.ops", fromlist=["ops"])
+    per_step = []
+    for i in range(args.warmup + args.steps):
+        v, sample = wl.cpu_sample(oracle, budget_s=3.0)
+        if i >= args.warmup:
+            per_step.append(v)
+    value = statistics.median(per_step)
+    line = {"impl": "reference", "metric": "int8 linear GB/s (algorithmic bytes)", "value": value, "unit": "GB/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8xint8->int32,f32", "data": "synthetic",
+            "config": wl.describe(),
+            "cpu_baseline": {"value": value, "unit": "GB/s", "cores": 1, "kind": "port", "sample": sample},
+            "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args, rank, world, local):
+    import torch
+
+    pkg = entry.load_package()
+    pkg.lib()
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    wl = WORKLOADS[args.workload]()
+    wl.setup(device)
+    stream = torch.cuda.current_stream()
+    for _ in range(args.warmup):
+        wl.step()
+    torch.cuda.synchronize()
+
+    # kernel-only timing: events around each step on the launching stream
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    barrier(world)
+    torch.cuda.synchronize()
+    launches = 0
+    with ClockSampler(torch.cuda.current_device()) as clocks:
+        t_begin = torch.cuda.Event(enable_timing=True)
+        t_end = torch.cuda.Event(enable_timing=True)
+        t_begin.record(stream)
+        for i in range(args.steps):
+            starts[i].record(stream)
+            launches += wl.step()
+            ends[i].record(stream)
+        t_end.record(stream)
+        torch.cuda.synchronize()
+    barrier(world)
+    total_ms = t_begin.elapsed_time(t_end)
+    per_launch_ms = statistics.mean(s.elapsed_time(e) for s, e in zip(starts, ends))
+    total_ms = max_over_ranks(total_ms, world)
+    ms_per_step = total_ms / args.steps
+    value = world * wl.units_per_step() * wl.unit_bytes / (ms_per_step * 1e-3) / 1e9
+
+    # end to end through the public API with host buffers
+    for _ in range(3):
+        wl.e2e_step()
+    torch.cuda.synchronize()
+    barrier(world)
+    e_begin = torch.cuda.Event(enable_timing=True)
+    e_end = torch.cuda.Event(enable_timing=True)
+    e_steps = max(args.steps, 20)
+    e_begin.record(stream)
+    h2d = d2h = 0
+    for _ in range(e_steps):
+        _, h2d, d2h = wl.e2e_step()
+    e_end.record(stream)
+    torch.cuda.synchronize()
+    e_ms = max_over_ranks(e_begin.elapsed_time(e_end) / e_steps, world)
+    e2e_value = world * wl.unit_bytes / (e_ms * 1e-3) / 1e9
+
+    peak, peak_kind = hbm_peak()
+    achieved = wl.bytes_per_step() / (per_launch_ms * 1e-3) / 1e9
+    line = {"metric": "int8 linear GB/s (algorithmic bytes)", "value": value, "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8xint8->int32,f32", "data": "synthetic",
+            "config": wl.describe(),
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": None, "peak_source": peak_kind,
+                         "kernel": "gemv_i8g32_kernel"},
+            "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "ms_per_call": e_ms},
+            "gpu_launches": launches,
+            "clocks": clocks.summary()}
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        oracle = entry.load_oracle()
+        v, sample = wl.cpu_sample(oracle)
+        line["cpu_baseline"] = {"value": v, "unit": "GB/s", "cores": 1, "kind": "port", "sample": sample}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="cfg1")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    rank, world, local = (int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")),
+                          int(os.environ.get("LOCAL_RANK", "0")))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+    rank, world, local = dist_setup(args.gpus)
+    try:
+        run_ours(args, rank, world, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,143 @@
+/*
+ * needle_cuda.h - C ABI of the B200 (sm_100a) batched quantized decode path
+ * for needle-cs.
+ *
+ * Plain C: pointers, sizes and int status codes; no CUDA or torch types.
+ * A `stream` argument is a cudaStream_t passed as void* (NULL = legacy
+ * default stream).  Functions named ndl_kt_* take HOST pointers and are
+ * synchronous: they have the exact signatures of the reference's
+ * KernelTable slots (src/Needle/Kernels/KernelTable.cs:5-47, signatures
+ * fixed by src/Needle/Kernels/Net10KernelExports.cs:118-150) so that the C#
+ * engine can install them with Kernels.Install.  Every other compute entry
+ * point takes DEVICE pointers and is stream-ordered (asynchronous).
+ *
+ * Errors never cross the ABI as exceptions.  Codes 1..11 mirror the
+ * reference's FailureReason (src/Needle/Reply.cs:8-22); codes >= 100 are
+ * library errors.  ndl_last_error() returns a per-thread message for the
+ * last non-zero status.
+ */
+#ifndef NEEDLE_CUDA_H
+#define NEEDLE_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(_WIN32)
+#define NDL_API __declspec(dllexport)
+#else
+#define NDL_API __attribute__((visibility("default")))
+#endif
+
+/* ------------------------------------------------------------------ */
+/* Status codes                                                        */
+/* ------------------------------------------------------------------ */
+enum {
+    NDL_OK = 0,
+    /* FailureReason mirror (src/Needle/Reply.cs:8-22) */
+    NDL_FAIL_EMPTY_INPUT = 1,
+    NDL_FAIL_INPUT_TOO_LONG = 2,
+    NDL_FAIL_CONTEXT_EXHAUSTED = 3,
+    NDL_FAIL_CALL_TOKEN_BUDGET = 4,
+    NDL_FAIL_CALL_TEXT_TOO_LONG = 5,
+    NDL_FAIL_GRAMMAR_DEAD_END = 6,
+    NDL_FAIL_GRAMMAR_REJECTED = 7,
+    NDL_FAIL_CALLS_BUFFER = 8,
+    NDL_FAIL_MALFORMED_CALLS = 9,
+    NDL_FAIL_TOOL_CONTEXT = 10,
+    NDL_FAIL_FRAME_BUDGET = 11,
+    /* library errors */
+    NDL_ERR_INVALID_ARG = 100,
+    NDL_ERR_CUDA = 101,
+    NDL_ERR_BOUNDS = 102,
+    NDL_ERR_TIMEOUT = 103,
+    NDL_ERR_OUT_OF_MEMORY = 104,
+    NDL_ERR_UNSUPPORTED = 105,
+    NDL_ERR_NO_DEVICE = 106,
+    NDL_ERR_MALFORMED_MODEL = 107,
+    NDL_ERR_PAGES_EXHAUSTED = 108,
+    NDL_ERR_CANCELLED = 109
+};
+
+/* Library identity and diagnostics (no reference counterpart). */
+NDL_API const char *ndl_version(void);
+NDL_API const char *ndl_status_string(int status);
+NDL_API const char *ndl_last_error(void);
+NDL_API int ndl_device_count(int *count);
+
+/* ------------------------------------------------------------------ */
+/* Synthetic inputs                                                    */
+/* ------------------------------------------------------------------ */
+/* Counter-based generator used for every synthetic workload.  Value i of
+ * stream s under seed k is a pure function of (k, s, i), so host and device
+ * produce identical bits:
+ *   key     = splitmix64(k ^ (s * 0x9E3779B97F4A7C15))
+ *   h(i)    = splitmix64(key + i * 0xD1B54A32D192ED03)
+ *   normal  = (2*S - 786420) / 131072, S = sum of the twelve 16-bit fields
+ *             of h(3i), h(3i+1), h(3i+2)     (Irwin-Hall(12) - 6, var 1)
+ *   uniform = lo + (hi - lo) * float(h(i) >> 40) * 2^-24
+ *   int8    = int(h(i) % 255) - 127            (U{-127..127})
+ *   fp16    = round-to-nearest-even of a float
+ * The reference's own test RNG (XorShift64, tests/Needle.Tests/Conformance/
+ * Conformance.cs:10-38) drives only the conformance-case ports. */
+NDL_API void ndl_synth_normal_f32(uint64_t seed, uint64_t stream, uint64_t first, size_t count, float scale,
+                                  float *out);
+NDL_API void ndl_synth_normal_f16(uint64_t seed, uint64_t stream, uint64_t first, size_t count, float scale,
+                                  uint16_t *out);
+NDL_API void ndl_synth_uniform_f16(uint64_t seed, uint64_t stream, uint64_t first, size_t count, float lo,
+                                   float hi, uint16_t *out);
+NDL_API void ndl_synth_int8(uint64_t seed, uint64_t stream, uint64_t first, size_t count, int8_t *out);
+NDL_API uint16_t ndl_f32_to_f16(float value);
+NDL_API float ndl_f16_to_f32(uint16_t half);
+/* Device-side fills (same bits as the host functions). */
+NDL_API int ndl_synth_normal_f32_device(uint64_t seed, uint64_t stream, uint64_t first, size_t count, float scale,
+                                        float *out, void *cuda_stream);
+NDL_API int ndl_synth_normal_f16_device(uint64_t seed, uint64_t stream, uint64_t first, size_t count,
+                                        float scale, uint16_t *out, void *cuda_stream);
+NDL_API int ndl_synth_uniform_f16_device(uint64_t seed, uint64_t stream, uint64_t first, size_t count, float lo,
+                                         float hi, uint16_t *out, void *cuda_stream);
+NDL_API int ndl_synth_int8_device(uint64_t seed, uint64_t stream, uint64_t first, size_t count, int8_t *out,
+                                  void *cuda_stream);
+
+/* ------------------------------------------------------------------ */
+/* Device kernels (device pointers, stream-ordered)                    */
+/* ------------------------------------------------------------------ */
+
+/* Per-row int8 quantizer.  Replaces Quant.QuantizeInt8
+ * (src/Needle/Quant.cs:103-132; scalar definition src/Needle/Scalar.cs:67-74)
+ * applied to each row of x [rows][cols]: scale = max|x|/127 (1 if zero),
+ * q = clamp(round_half_even(x * (1/scale)), -128, 127).  Bit-exact. */
+NDL_API int ndl_quantize_rows(const float *x, int rows, int cols, int8_t *q, float *scales, void *stream);
+
+/* Fused RMSNorm + quantizer for the synthetic decoder: h = (w*x)*inv_rms(x)
+ * (eps 1e-6, src/Needle/Ops.cs:12,209,233-255), then ndl_quantize_rows(h). */
+NDL_API int ndl_rmsnorm_quantize(const float *x, const float *weight, int rows, int cols, int8_t *q, float *scales,
+                                 void *stream);
+
+/* I8G32 quantized linear.  Replaces Quant.MatMulRows
+ * (src/Needle/Quant.cs:615-633 -> src/Needle/Gemv.cs:117-333; scalar
+ * definition src/Needle/Scalar.cs:146-192) for int8 weights with one fp16
+ * scale per (row, 32-column group):
+ *   D[t][n][g] = sum_{k in g} w[n][k]*q[t][k]            (int32, exact)
+ *   y[t][n]    = (residual ? residual[t][n] : 0) + sum_g (half(sw[n][g]) * sa[t]) * float(D)
+ * with g ascending and no fused multiply-add, so y is bit-identical to the
+ * scalar definition whatever the batch size.  acc (nullable) receives D as
+ * [m][n][k/32].  k must be a multiple of 32; w, q 16-byte aligned.
+ * M < 64 runs the streaming GEMV; M >= 64 the tcgen05 kind::i8 GEMM. */
+NDL_API int ndl_matmul_i8g32(const int8_t *q, const float *sa, int m, const int8_t *w, const uint16_t *sw, int n,
+                             int k, float *y, int ldy, const float *residual, int32_t *acc, void *stream);
+
+/* The same linear over `batch` independent weight sets sharing one set of
+ * activations (MatMulBatch, src/Needle/Quant.cs:679-816): set b uses
+ * w + b*w_stride, sw + b*sw_stride and writes y + b*y_stride. */
+NDL_API int ndl_matmul_i8g32_batched(const int8_t *q, const float *sa, int m, const int8_t *w,
+                                     const uint16_t *sw, int n, int k, int batch, long long w_stride,
+                                     long long sw_stride, float *y, int ldy, long long y_stride, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,72 @@
+"""ctypes binding of libneedle_b200.so (the C ABI in include/needle_cuda.h).
+
+The library is built in-tree (needle-cs_b200/lib/) by `make -C needle-cs_b200`.
+There is no fallback: if the library is missing every call raises.
+"""
+import ctypes
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "lib", "libneedle_b200.so")
+
+c_int, c_float, c_size_t, c_u64, c_ll = ctypes.c_int, ctypes.c_float, ctypes.c_size_t, ctypes.c_uint64, ctypes.c_longlong
+c_void_p, c_char_p = ctypes.c_void_p, ctypes.c_char_p
+c_u16 = ctypes.c_uint16
+
+# name -> (restype, argtypes).  Device pointers and streams travel as void*.
+SIGNATURES = {
+    "ndl_version": (c_char_p, []),
+    "ndl_status_string": (c_char_p, [c_int]),
+    "ndl_last_error": (c_char_p, []),
+    "ndl_device_count": (c_int, [ctypes.POINTER(c_int)]),
+    "ndl_synth_normal_f32": (None, [c_u64, c_u64, c_u64, c_size_t, c_float, c_void_p]),
+    "ndl_synth_normal_f16": (None, [c_u64, c_u64, c_u64, c_size_t, c_float, c_void_p]),
+    "ndl_synth_uniform_f16": (None, [c_u64, c_u64, c_u64, c_size_t, c_float, c_float, c_void_p]),
+    "ndl_synth_int8": (None, [c_u64, c_u64, c_u64, c_size_t, c_void_p]),
+    "ndl_f32_to_f16": (c_u16, [c_float]),
+    "ndl_f16_to_f32": (c_float, [c_u16]),
+    "ndl_synth_normal_f32_device": (c_int, [c_u64, c_u64, c_u64, c_size_t, c_float, c_void_p, c_void_p]),
+    "ndl_synth_normal_f16_device": (c_int, [c_u64, c_u64, c_u64, c_size_t, c_float, c_void_p, c_void_p]),
+    "ndl_synth_uniform_f16_device": (c_int, [c_u64, c_u64, c_u64, c_size_t, c_float, c_float, c_void_p, c_void_p]),
+    "ndl_synth_int8_device": (c_int, [c_u64, c_u64, c_u64, c_size_t, c_void_p, c_void_p]),
+    "ndl_quantize_rows": (c_int, [c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p]),
+    "ndl_rmsnorm_quantize": (c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p]),
+    "ndl_matmul_i8g32": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_int, c_int, c_void_p, c_int,
+                                 c_void_p, c_void_p, c_void_p]),
+    "ndl_matmul_i8g32_batched": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_int, c_int, c_int, c_ll,
+                                         c_ll, c_void_p, c_int, c_ll, c_void_p]),
+}
+
+
+class NeedleError(RuntimeError):
+    def __init__(self, status, message):
+        super().__init__(f"needle status {status}: {message}")
+        self.status = status
+
+
+_lib = None
+
+
+def lib():
+    """Load the native library once; raise loudly if it is not built."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(f"needle_cs_b200 native library not built: {LIB_PATH} (run make -C needle-cs_b200)")
+        handle = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(handle, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = handle
+    return _lib
+
+
+def check(status):
+    if status != 0:
+        raise NeedleError(status, lib().ndl_last_error().decode())
+    return status
+
+
+def call(name, *args):
+    return check(getattr(lib(), name)(*args))

@@ -1,0 +1,120 @@
+// Shared helpers for the needle B200 library: status plumbing, the
+// reference's fp16 decode, the counter-based synthetic generator, and small
+// PTX wrappers.  Everything here is used by host and device code alike.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/needle_cuda.h"
+
+namespace ndl {
+
+// ---------------------------------------------------------------- status --
+// Records a per-thread message for ndl_last_error() and returns `status`.
+int set_error(int status, const char *fmt, ...);
+// Converts the last CUDA error (launch or sticky) into a status.
+int check_launch(const char *what);
+
+#define NDL_REQUIRE(cond, ...)                                                   \
+    do {                                                                         \
+        if (!(cond)) return ::ndl::set_error(NDL_ERR_INVALID_ARG, __VA_ARGS__); \
+    } while (0)
+
+#define NDL_CUDA(call)                                                                          \
+    do {                                                                                        \
+        cudaError_t e_ = (call);                                                                \
+        if (e_ != cudaSuccess)                                                                  \
+            return ::ndl::set_error(NDL_ERR_CUDA, "%s: %s", #call, cudaGetErrorString(e_));     \
+    } while (0)
+
+inline bool aligned(const void *p, size_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
+
+// ------------------------------------------------------------------ fp16 --
+// Scalar.HalfToSingle (src/Needle/Scalar.cs:121-128): exact for finite
+// halves, no Inf/NaN case (0x7C00 -> 65536).  Integer-only so host and
+// device agree bit for bit.
+__host__ __device__ __forceinline__ float half_to_float_ref(uint16_t half) {
+    uint32_t magnitude = half & 0x7FFFu;
+    if (magnitude == 0) return 0.0f;
+    if (magnitude < 0x0400u) {
+        float v = (float)magnitude * 5.9604645e-8f;
+        return (half & 0x8000u) ? -v : v;
+    }
+    uint32_t bits = ((magnitude << 13) + 0x38000000u) | ((uint32_t)(half & 0x8000u) << 16);
+#ifdef __CUDA_ARCH__
+    return __uint_as_float(bits);
+#else
+    float f;
+    __builtin_memcpy(&f, &bits, 4);
+    return f;
+#endif
+}
+
+// IEEE round-to-nearest-even float -> binary16 (integer-only).
+__host__ __device__ __forceinline__ uint16_t float_to_half_rne(float f) {
+#ifdef __CUDA_ARCH__
+    uint32_t x = __float_as_uint(f);
+#else
+    uint32_t x;
+    __builtin_memcpy(&x, &f, 4);
+#endif
+    uint32_t sign = (x >> 16) & 0x8000u;
+    uint32_t abs = x & 0x7FFFFFFFu;
+    if (abs >= 0x7F800000u) return (uint16_t)(sign | (abs > 0x7F800000u ? 0x7E00u : 0x7C00u));
+    if (abs >= 0x477FF000u) return (uint16_t)(sign | 0x7C00u);  // rounds to >= 65520 -> inf
+    if (abs < 0x38800000u) {                                     // subnormal or zero in half
+        if (abs < 0x33000000u) return (uint16_t)sign;            // < 2^-25 rounds to 0
+        uint32_t mant = (abs & 0x007FFFFFu) | 0x00800000u;
+        int shift = 126 - (int)(abs >> 23);                      // 14 + (113 - exp) ... >= 14
+        // value = mant * 2^(exp-150); half subnormal unit = 2^-24 -> q = mant >> (126 - exp)
+        uint32_t q = mant >> shift;
+        uint32_t rem = mant & ((1u << shift) - 1u);
+        uint32_t halfway = 1u << (shift - 1);
+        if (rem > halfway || (rem == halfway && (q & 1u))) q++;
+        return (uint16_t)(sign | q);
+    }
+    uint32_t rebased = abs - 0x38000000u;  // exponent bias 127 -> 15
+    uint32_t q = rebased >> 13;
+    uint32_t rem = rebased & 0x1FFFu;
+    if (rem > 0x1000u || (rem == 0x1000u && (q & 1u))) q++;
+    return (uint16_t)(sign | q);
+}
+
+// ------------------------------------------------------ synthetic inputs --
+__host__ __device__ __forceinline__ uint64_t splitmix64(uint64_t z) {
+    z += 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+__host__ __device__ __forceinline__ uint64_t synth_key(uint64_t seed, uint64_t stream) {
+    return splitmix64(seed ^ (stream * 0x9E3779B97F4A7C15ull));
+}
+__host__ __device__ __forceinline__ uint64_t synth_hash(uint64_t key, uint64_t i) {
+    return splitmix64(key + i * 0xD1B54A32D192ED03ull);
+}
+__host__ __device__ __forceinline__ int sum16x4(uint64_t h) {
+    return (int)(h & 0xFFFF) + (int)((h >> 16) & 0xFFFF) + (int)((h >> 32) & 0xFFFF) + (int)(h >> 48);
+}
+// Irwin-Hall(12) - 6 in exact arithmetic: identical on host and device.
+__host__ __device__ __forceinline__ float synth_normal(uint64_t key, uint64_t i) {
+    int s = sum16x4(synth_hash(key, 3 * i)) + sum16x4(synth_hash(key, 3 * i + 1)) +
+            sum16x4(synth_hash(key, 3 * i + 2));
+    return (float)(2 * s - 786420) * (1.0f / 131072.0f);
+}
+__host__ __device__ __forceinline__ float synth_uniform(uint64_t key, uint64_t i, float lo, float hi) {
+    float u = (float)(synth_hash(key, i) >> 40) * (1.0f / 16777216.0f);
+#ifdef __CUDA_ARCH__
+    return __fadd_rn(lo, __fmul_rn(__fsub_rn(hi, lo), u));  // no contraction: matches the host
+#else
+    float span = hi - lo;
+    float t = span * u;
+    return lo + t;
+#endif
+}
+__host__ __device__ __forceinline__ int8_t synth_int8(uint64_t key, uint64_t i) {
+    return (int8_t)((int)(synth_hash(key, i) % 255u) - 127);
+}
+
+}  // namespace ndl

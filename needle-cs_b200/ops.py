@@ -1,0 +1,116 @@
+"""Tensor-level wrappers over the C ABI.
+
+torch is plumbing here: device memory, the current CUDA stream and shape
+bookkeeping.  All arithmetic happens in libneedle_b200.so.  Every wrapper
+checks device, dtype and contiguity before handing raw pointers to the ABI.
+"""
+import numpy as np
+import torch
+
+from ._native import call, lib
+
+
+def _stream():
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _dev(t, dtype, name):
+    if not isinstance(t, torch.Tensor) or not t.is_cuda:
+        raise TypeError(f"{name} must be a CUDA tensor")
+    if t.dtype != dtype:
+        raise TypeError(f"{name} must be {dtype}, got {t.dtype}")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+    return t.data_ptr()
+
+
+# ---------------------------------------------------------------- synth --
+
+def synth_normal_f32(seed, stream, count, scale=1.0, first=0):
+    out = np.empty(count, np.float32)
+    lib().ndl_synth_normal_f32(seed, stream, first, count, scale, out.ctypes.data)
+    return out
+
+
+def synth_normal_f16(seed, stream, count, scale=1.0, first=0):
+    out = np.empty(count, np.uint16)
+    lib().ndl_synth_normal_f16(seed, stream, first, count, scale, out.ctypes.data)
+    return out
+
+
+def synth_uniform_f16(seed, stream, count, lo, hi, first=0):
+    out = np.empty(count, np.uint16)
+    lib().ndl_synth_uniform_f16(seed, stream, first, count, lo, hi, out.ctypes.data)
+    return out
+
+
+def synth_int8(seed, stream, count, first=0):
+    out = np.empty(count, np.int8)
+    lib().ndl_synth_int8(seed, stream, first, count, out.ctypes.data)
+    return out
+
+
+def synth_normal_f32_device(seed, stream, out, scale=1.0, first=0):
+    call("ndl_synth_normal_f32_device", seed, stream, first, out.numel(), scale, _dev(out, torch.float32, "out"),
+         _stream())
+
+
+def synth_normal_f16_device(seed, stream, out, scale=1.0, first=0):
+    call("ndl_synth_normal_f16_device", seed, stream, first, out.numel(), scale, _dev(out, torch.int16, "out"),
+         _stream())
+
+
+def synth_uniform_f16_device(seed, stream, out, lo, hi, first=0):
+    call("ndl_synth_uniform_f16_device", seed, stream, first, out.numel(), lo, hi, _dev(out, torch.int16, "out"),
+         _stream())
+
+
+def synth_int8_device(seed, stream, out, first=0):
+    call("ndl_synth_int8_device", seed, stream, first, out.numel(), _dev(out, torch.int8, "out"), _stream())
+
+
+# -------------------------------------------------------------- kernels --
+
+def quantize_rows(x, q=None, scales=None):
+    """Per-row int8 quantizer (Quant.QuantizeInt8 per row)."""
+    rows, cols = x.shape
+    q = torch.empty((rows, cols), dtype=torch.int8, device=x.device) if q is None else q
+    scales = torch.empty(rows, dtype=torch.float32, device=x.device) if scales is None else scales
+    call("ndl_quantize_rows", _dev(x, torch.float32, "x"), rows, cols, _dev(q, torch.int8, "q"),
+         _dev(scales, torch.float32, "scales"), _stream())
+    return q, scales
+
+
+def rmsnorm_quantize(x, weight, q=None, scales=None):
+    rows, cols = x.shape
+    q = torch.empty((rows, cols), dtype=torch.int8, device=x.device) if q is None else q
+    scales = torch.empty(rows, dtype=torch.float32, device=x.device) if scales is None else scales
+    call("ndl_rmsnorm_quantize", _dev(x, torch.float32, "x"), _dev(weight, torch.float32, "weight"), rows, cols,
+         _dev(q, torch.int8, "q"), _dev(scales, torch.float32, "scales"), _stream())
+    return q, scales
+
+
+def matmul_i8g32(q, sa, w, sw, y=None, residual=None, acc=None):
+    """I8G32 linear: y[t][n] = sum_g (half(sw[n][g]) * sa[t]) * D[t][n][g].
+
+    q int8 [m,k], sa fp32 [m], w int8 [n,k], sw fp16 bits as int16 [n,k/32].
+    """
+    m, k = q.shape
+    n = w.shape[0]
+    y = torch.empty((m, n), dtype=torch.float32, device=q.device) if y is None else y
+    res_ptr = _dev(residual, torch.float32, "residual") if residual is not None else None
+    acc_ptr = _dev(acc, torch.int32, "acc") if acc is not None else None
+    call("ndl_matmul_i8g32", _dev(q, torch.int8, "q"), _dev(sa, torch.float32, "sa"), m,
+         _dev(w, torch.int8, "w"), _dev(sw, torch.int16, "sw"), n, k, _dev(y, torch.float32, "y"), y.stride(0),
+         res_ptr, acc_ptr, _stream())
+    return y
+
+
+def matmul_i8g32_batched(q, sa, w, sw, y):
+    """Batched I8G32 linear over weight sets w [B,n,k], sw [B,n,k/32] -> y [B,m,n]."""
+    m, k = q.shape
+    batch, n, _ = w.shape
+    call("ndl_matmul_i8g32_batched", _dev(q, torch.int8, "q"), _dev(sa, torch.float32, "sa"), m,
+         _dev(w, torch.int8, "w"), _dev(sw, torch.int16, "sw"), n, k, batch, n * k, n * (k // 32),
+         _dev(y, torch.float32, "y"), n, m * n, _stream())
+    return y

@@ -1,0 +1,599 @@
+/*
+ * needle_oracle.c - CPU restatement of the needle-cs batched decode path.
+ *
+ * TEST INFRASTRUCTURE ONLY: the parity checker for the CUDA library, never
+ * linked into it.  Each function cites the reference routine it restates
+ * (paths relative to the needle-cs source tree).  Build with
+ * -ffp-contract=off so that a*b+c stays two rounded operations, as in the
+ * reference's scalar C#.
+ */
+#include "needle_oracle.h"
+
+#include <math.h>
+#include <stdlib.h>
+#include <string.h>
+
+/* ------------------------------------------------------------------------ */
+/* Test-input generators: tests/Needle.Tests/Conformance/Conformance.cs      */
+/* ------------------------------------------------------------------------ */
+
+/* XorShift64.Next (Conformance.cs:19-27); seed 0 is replaced by the golden
+ * ratio constant (Conformance.cs:14-17) by the caller. */
+uint64_t ndo_xorshift_next(uint64_t *state) {
+    uint64_t x = *state;
+    x ^= x << 13;
+    x ^= x >> 7;
+    x ^= x << 17;
+    *state = x;
+    return x;
+}
+
+/* XorShift64.NextInt (Conformance.cs:29-32). */
+int ndo_xorshift_int(uint64_t *state, int lo, int hi) {
+    return lo + (int)(ndo_xorshift_next(state) % (uint64_t)(hi - lo));
+}
+
+/* XorShift64.NextFloat (Conformance.cs:34-37): ulong->float, then float ops. */
+float ndo_xorshift_float(uint64_t *state, float scale) {
+    float u = (float)(ndo_xorshift_next(state) >> 11) * (1.0f / 9007199254740992.0f);
+    return ((u - 0.5f) * 2.0f) * scale;
+}
+
+/* ConformanceInputs.FillUniform (Conformance.cs:42-48). */
+void ndo_fill_uniform(float *x, int n, uint64_t *state, float scale) {
+    for (int i = 0; i < n; i++) x[i] = ndo_xorshift_float(state, scale);
+}
+
+/* ConformanceInputs.FillEdges (Conformance.cs:50-68): zeros every 7th,
+ * +-1e-38 denormals every 11th from 3, +-0.5*scale ties every 13th from 5. */
+void ndo_fill_edges(float *x, int n, uint64_t *state, float scale) {
+    for (int i = 0; i < n; i++) x[i] = ndo_xorshift_float(state, scale);
+    for (int i = 0; i < n; i += 7) x[i] = 0.0f;
+    for (int i = 3; i < n; i += 11) x[i] = 1e-38f * (i % 2 == 0 ? 1.0f : -1.0f);
+    for (int i = 5; i < n; i += 13) x[i] = (i % 26 < 13 ? 0.5f : -0.5f) * scale;
+}
+
+/* ConformanceInputs.FillSByte (Conformance.cs:70-88). */
+void ndo_fill_sbyte(int8_t *x, int n, uint64_t *state, int extremes) {
+    for (int i = 0; i < n; i++) x[i] = (int8_t)ndo_xorshift_int(state, -128, 128);
+    if (extremes && n > 0) {
+        x[0] = -128;
+        if (n > 1) x[1] = 127;
+        for (int i = 2; i < n; i += 5) x[i] = (i % 2 == 0) ? (int8_t)-128 : (int8_t)127;
+    }
+}
+
+/* ConformanceInputs.FillBytes (Conformance.cs:90-101). */
+void ndo_fill_bytes(uint8_t *x, int n, uint64_t *state, int extremes) {
+    for (int i = 0; i < n; i++) x[i] = (uint8_t)ndo_xorshift_int(state, 0, 256);
+    if (extremes && n >= 2) {
+        x[0] = 0x00;
+        x[1] = 0xFF;
+    }
+}
+
+/* ConformanceInputs.HalfBits (Conformance.cs:103-118): saturating, flush
+ * below 2^-15, round-half-up on the dropped 13 bits. */
+uint16_t ndo_half_bits(float value) {
+    uint32_t bits;
+    memcpy(&bits, &value, 4);
+    uint32_t sign = (bits >> 16) & 0x8000u;
+    uint32_t magnitude = bits & 0x7FFFFFFFu;
+    if (magnitude >= 0x47800000u) return (uint16_t)(sign | 0x7BFFu);
+    if (magnitude <= 0x38000000u) return (uint16_t)sign;
+    uint32_t rounded = (magnitude >> 13) + ((magnitude >> 12) & 1u);
+    return (uint16_t)(sign | (rounded - 0x1C000u));
+}
+
+/* ------------------------------------------------------------------------ */
+/* Row primitives: src/Needle/Scalar.cs                                      */
+/* ------------------------------------------------------------------------ */
+
+static const float kRoundBias = 12582912.0f;           /* Scalar.cs:51 */
+static const float kHadamardScale = 0.08838834764831845f; /* Scalar.cs:49 */
+
+/* Scalar.RoundEven (Scalar.cs:52-53): the 1.5*2^23 trick. */
+static float round_even(float x) {
+    volatile float t = x + kRoundBias; /* volatile keeps the two roundings */
+    return t - kRoundBias;
+}
+
+static float maxf_cs(float a, float b) { return a > b ? a : (b > a ? b : (a == a ? a : b)); }
+
+/* Scalar.AbsMax (Scalar.cs:55-60). */
+float ndo_abs_max(const float *x, int n) {
+    float peak = 0.0f;
+    for (int i = 0; i < n; i++) peak = maxf_cs(peak, fabsf(x[i]));
+    return peak;
+}
+
+static float clamp_q(float v) { return fminf(fmaxf(v, -128.0f), 127.0f); }
+
+/* Scalar.QuantizeInt8 (Scalar.cs:67-74). */
+float ndo_quantize_int8(const float *x, int n, int8_t *dst) {
+    float peak = ndo_abs_max(x, n);
+    float scale = peak > 0.0f ? peak / 127.0f : 1.0f;
+    float inverse = 1.0f / scale;
+    for (int i = 0; i < n; i++) dst[i] = (int8_t)clamp_q(round_even(x[i] * inverse));
+    return scale;
+}
+
+/* Per-row QuantizeInt8 over a [rows][cols] matrix (the activation quantizer
+ * applied to every linear input row, src/Needle/Quant.cs:103-132). */
+void ndo_quantize_rows(const float *x, int rows, int cols, int8_t *q, float *scales) {
+    for (int r = 0; r < rows; r++) scales[r] = ndo_quantize_int8(x + (size_t)r * cols, cols, q + (size_t)r * cols);
+}
+
+/* Quant.FakeA8 scalar path = AbsMax + Scalar.RoundTrip (Quant.cs:66-77,
+ * Scalar.cs:62-65). */
+float ndo_fake_a8(float *x, int n) {
+    float peak = ndo_abs_max(x, n);
+    float scale = peak > 0.0f ? peak / 127.0f : 1.0f;
+    float inverse = 1.0f / scale;
+    for (int i = 0; i < n; i++) x[i] = clamp_q(round_even(x[i] * inverse)) * scale;
+    return scale;
+}
+
+/* Scalar.HalfToSingle (Scalar.cs:121-128): subnormals exact, no Inf/NaN
+ * special case (0x7C00 decodes to 65536). */
+float ndo_half_to_single(uint16_t half) {
+    uint32_t magnitude = half & 0x7FFFu;
+    if (magnitude == 0) return 0.0f;
+    if (magnitude < 0x0400u)
+        return (half & 0x8000u) ? -(float)magnitude * 5.9604645e-8f : (float)magnitude * 5.9604645e-8f;
+    uint32_t bits = ((magnitude << 13) + 0x38000000u) | ((uint32_t)(half & 0x8000u) << 16);
+    float f;
+    memcpy(&f, &bits, 4);
+    return f;
+}
+
+/* Scalar.Hadamard (Scalar.cs:76-89): in-place FWHT over 128, then scale. */
+void ndo_hadamard128(const float *src, float *p) {
+    if (src != p)
+        for (int i = 0; i < 128; i++) p[i] = src[i];
+    for (int stride = 1; stride < 128; stride <<= 1)
+        for (int block = 0; block < 128; block += stride * 2)
+            for (int i = block; i < block + stride; i++) {
+                float a = p[i], b = p[i + stride];
+                p[i] = a + b;
+                p[i + stride] = a - b;
+            }
+    for (int i = 0; i < 128; i++) p[i] *= kHadamardScale;
+}
+
+/* Scalar.Planes (Scalar.cs:91-111). */
+void ndo_planes(const int8_t *quantized, int bits, int8_t *dst, int *sum) {
+    int s = 0;
+    if (bits == 2) {
+        for (int j = 0; j < 32; j++)
+            for (int p = 0; p < 4; p++) {
+                int8_t q = quantized[4 * j + p];
+                dst[p * 32 + j] = q;
+                s += q;
+            }
+    } else {
+        for (int half = 0; half < 2; half++)
+            for (int j = 0; j < 32; j++)
+                for (int p = 0; p < 2; p++) {
+                    int8_t q = quantized[half * 64 + 2 * j + p];
+                    dst[half * 64 + p * 32 + j] = q;
+                    s += q;
+                }
+    }
+    *sum = s;
+}
+
+/* Scalar.Sigmoid (Scalar.cs:194). */
+float ndo_sigmoid(float x) { return 1.0f / (1.0f + expf(-x)); }
+
+/* Scalar.Softmax (Scalar.cs:220-231). */
+void ndo_softmax(float *s, int n) {
+    float peak = -INFINITY;
+    for (int i = 0; i < n; i++) peak = maxf_cs(peak, s[i]);
+    float total = 0.0f;
+    for (int i = 0; i < n; i++) {
+        s[i] = expf(s[i] - peak);
+        total += s[i];
+    }
+    for (int i = 0; i < n; i++) s[i] /= total;
+}
+
+/* Scalar.Rope (Scalar.cs:233-248): half-split rotation. */
+void ndo_rope(float *x, int heads, int head_dim, const float *cos_t, const float *sin_t) {
+    int half = head_dim / 2;
+    for (int h = 0; h < heads; h++) {
+        float *lo = x + h * head_dim, *hi = lo + half;
+        for (int i = 0; i < half; i++) {
+            float a = lo[i], b = hi[i];
+            lo[i] = a * cos_t[i] - b * sin_t[i];
+            hi[i] = b * cos_t[i] + a * sin_t[i];
+        }
+    }
+}
+
+/* EngineCore.RopeFrequencies + BuildRopeTables (src/Needle/Engine.cs:336-356). */
+void ndo_rope_tables(float theta, int qk_dim, int positions, float *cos_t, float *sin_t) {
+    int half = qk_dim / 2;
+    float freq[512];
+    for (int i = 0; i < half && i < 512; i++) freq[i] = 1.0f / powf(theta, 2.0f * (float)i / (float)qk_dim);
+    for (int p = 0; p < positions; p++)
+        for (int i = 0; i < half; i++) {
+            float angle = (float)p * freq[i];
+            cos_t[(size_t)p * half + i] = cosf(angle);
+            sin_t[(size_t)p * half + i] = sinf(angle);
+        }
+}
+
+/* Ops.InverseRms (src/Needle/Ops.cs:209) over Scalar.SumOfSquares
+ * (Scalar.cs:206-211), epsilon 1e-6 (Ops.cs:12). */
+float ndo_inverse_rms(const float *x, int n) {
+    float sum = 0.0f;
+    for (int i = 0; i < n; i++) sum += x[i] * x[i];
+    return 1.0f / sqrtf(sum / (float)n + 1e-6f);
+}
+
+/* Synthetic RMSNorm: the scalar ZeroCenteredRms expression
+ * (src/Needle/Ops.cs:233-255, (1+scale)*x*inv) with a plain weight w in
+ * place of (1+scale): dst = (w*x)*inv. */
+void ndo_rms_norm(const float *x, const float *weight, int n, float *dst) {
+    float inv = ndo_inverse_rms(x, n);
+    for (int i = 0; i < n; i++) dst[i] = (weight[i] * x[i]) * inv;
+}
+
+/* Ops.ZeroCenteredRms scalar branch (src/Needle/Ops.cs:243). */
+void ndo_zero_centered_rms(const float *x, const float *scale, int n, float *dst) {
+    float inv = ndo_inverse_rms(x, n);
+    for (int i = 0; i < n; i++) dst[i] = ((1.0f + scale[i]) * x[i]) * inv;
+}
+
+/* SwiGLU from Scalar.Silu and Scalar.Glu (Scalar.cs:196-199,280-283):
+ * dst = (g*sigmoid(g))*u. */
+void ndo_swiglu(const float *gate, const float *up, int n, float *dst) {
+    for (int i = 0; i < n; i++) dst[i] = (gate[i] * ndo_sigmoid(gate[i])) * up[i];
+}
+
+/* ------------------------------------------------------------------------ */
+/* Quantized matmul                                                          */
+/* ------------------------------------------------------------------------ */
+
+/* Codebook.Fill (src/Needle/Model.cs:44-52); MathF.Round is half-to-even. */
+void ndo_codebook_fill(ndo_codebook *book, const float *levels, int count) {
+    float peak = 0.0f;
+    for (int i = 0; i < count; i++) peak = maxf_cs(peak, fabsf(levels[i]));
+    book->byte_scale = peak / 63.0f;
+    for (int i = 0; i < 16; i++) book->levels[i] = levels[i % count];
+    for (int i = 0; i < 32; i++)
+        book->bytes[i] = i % 16 < count ? (uint8_t)(rintf(levels[i % 16] / book->byte_scale) + 63.0f) : 0;
+}
+
+/* Quant.PrepareRange scalar branch (src/Needle/Quant.cs:471-484): per
+ * 128-group FWHT, int8 quantize, plane reorder, offset = 63*sum(q). */
+void ndo_prepare_cq(const float *x, int tokens, int cols, int bits, int8_t *values, float *scales,
+                    float *offsets, int stride) {
+    int groups = cols / 128;
+    float rotated[128];
+    int8_t quantized[128];
+    for (int t = 0; t < tokens; t++)
+        for (int g = 0; g < groups; g++) {
+            int slot = t * stride + g;
+            int sum;
+            ndo_hadamard128(x + (size_t)t * cols + g * 128, rotated);
+            scales[slot] = ndo_quantize_int8(rotated, 128, quantized);
+            ndo_planes(quantized, bits, values + ((size_t)t * groups + g) * 128, &sum);
+            offsets[slot] = 63.0f * (float)sum;
+        }
+}
+
+/* Scalar.MatMulRows (src/Needle/Scalar.cs:146-192). */
+void ndo_matmul_rows_cq(const uint8_t *indices, const uint16_t *norms, const ndo_codebook *book, int rows,
+                        int cols, int bits, const int8_t *values, const float *scales, const float *offsets,
+                        int stride, int tokens, float *y, int ldy, int row_start, int row_end) {
+    (void)rows;
+    int groups = cols / 128;
+    int row_bytes = cols * bits / 8;
+    const uint8_t *table = book->bytes;
+    float byte_scale = book->byte_scale;
+    for (int t = 0; t < tokens; t++) {
+        const int8_t *v = values + (size_t)t * cols;
+        const float *sc = scales + (size_t)t * stride;
+        const float *off = offsets + (size_t)t * stride;
+        for (int n = row_start; n < row_end; n++) {
+            const uint8_t *packed = indices + (size_t)n * row_bytes;
+            const uint16_t *nr = norms + (size_t)n * groups;
+            float accumulator = 0.0f, bias = 0.0f;
+            for (int g = 0; g < groups; g++) {
+                const int8_t *x = v + g * 128;
+                int dot = 0;
+                if (bits == 2) {
+                    const uint8_t *p = packed + g * 32;
+                    for (int j = 0; j < 32; j++) {
+                        int b = p[j];
+                        dot += table[b & 3] * x[j] + table[b >> 2 & 3] * x[32 + j] + table[b >> 4 & 3] * x[64 + j] +
+                               table[b >> 6 & 3] * x[96 + j];
+                    }
+                } else {
+                    const uint8_t *p = packed + g * 64;
+                    for (int half = 0; half < 2; half++)
+                        for (int j = 0; j < 32; j++) {
+                            int b = p[half * 32 + j];
+                            dot += table[b & 15] * x[2 * half * 32 + j] + table[b >> 4] * x[(2 * half + 1) * 32 + j];
+                        }
+                }
+                float scaled = (ndo_half_to_single(nr[g]) * byte_scale) * sc[g];
+                accumulator += scaled * (float)dot;
+                bias += scaled * off[g];
+            }
+            y[(size_t)t * ldy + n] = accumulator - bias;
+        }
+    }
+}
+
+/* I8G32: the Scalar.MatMulRows skeleton (Scalar.cs:146-192) with raw int8
+ * weights, 32-column groups and one activation scale per row. */
+void ndo_matmul_i8g32(const int8_t *w, const uint16_t *sw, int n_rows, int k, const int8_t *q, const float *sa,
+                      int m, int32_t *acc, float *y, int ldy) {
+    int groups = k / 32;
+    for (int t = 0; t < m; t++) {
+        const int8_t *x = q + (size_t)t * k;
+        for (int n = 0; n < n_rows; n++) {
+            const int8_t *row = w + (size_t)n * k;
+            const uint16_t *scales = sw + (size_t)n * groups;
+            float accumulator = 0.0f;
+            for (int g = 0; g < groups; g++) {
+                int dot = 0;
+                for (int j = 0; j < 32; j++) dot += row[g * 32 + j] * x[g * 32 + j];
+                if (acc) acc[((size_t)t * n_rows + n) * groups + g] = dot;
+                float scaled = ndo_half_to_single(scales[g]) * sa[t];
+                accumulator += scaled * (float)dot;
+            }
+            y[(size_t)t * ldy + n] = accumulator;
+        }
+    }
+}
+
+/* ------------------------------------------------------------------------ */
+/* Attention                                                                 */
+/* ------------------------------------------------------------------------ */
+
+/* Scalar.AttentionHead (src/Needle/Scalar.cs:290-312). */
+void ndo_attention_head(const int8_t *query, float query_scale, const int8_t *keys, const float *key_scales,
+                        const int8_t *values, const float *value_scales, int key_stride, int value_stride,
+                        int scale_stride, int first, int last, int qk_dim, int v_dim, float inv_sqrt_dim,
+                        float *scores, float *output, float *probabilities) {
+    int count = last - first + 1;
+    float scale = query_scale * inv_sqrt_dim;
+    for (int s = 0; s < count; s++) {
+        const int8_t *key = keys + (size_t)(first + s) * key_stride;
+        int dot = 0;
+        for (int d = 0; d < qk_dim; d++) dot += query[d] * key[d];
+        scores[s] = ((float)dot * key_scales[(size_t)(first + s) * scale_stride]) * scale;
+    }
+    ndo_softmax(scores, count);
+    if (probabilities)
+        for (int s = 0; s < count; s++) probabilities[first + s] = scores[s];
+    for (int d = 0; d < v_dim; d++) output[d] = 0.0f;
+    for (int s = 0; s < count; s++) {
+        const int8_t *row = values + (size_t)(first + s) * value_stride;
+        float weight = scores[s] * value_scales[(size_t)(first + s) * scale_stride];
+        for (int d = 0; d < v_dim; d++) output[d] += weight * (float)row[d];
+    }
+}
+
+/* Attention.MergePartials, non-SIMD branch (src/Needle/Blocks.cs:750-817). */
+void ndo_merge_partials(const float *partials, int count, int heads, int stride, int peak_off, float *output) {
+    float weights[64];
+    for (int h = 0; h < heads; h++) {
+        if (count == 2) {
+            float peak0 = partials[peak_off + h];
+            float peak1 = partials[stride + peak_off + h];
+            float pk = maxf_cs(peak0, peak1);
+            float w0 = expf(peak0 - pk), w1 = expf(peak1 - pk);
+            float tot = 0.0f;
+            tot += w0 * partials[peak_off + 8 + h];
+            tot += w1 * partials[stride + peak_off + 8 + h];
+            float inv = 1.0f / tot;
+            for (int d = 0; d < 64; d++)
+                output[h * 64 + d] = (w0 * partials[h * 64 + d] + w1 * partials[stride + h * 64 + d]) * inv;
+            continue;
+        }
+        float peak = -INFINITY;
+        for (int c = 0; c < count; c++) peak = maxf_cs(peak, partials[c * stride + peak_off + h]);
+        float total = 0.0f;
+        for (int c = 0; c < count; c++) {
+            weights[c] = expf(partials[c * stride + peak_off + h] - peak);
+            total += weights[c] * partials[c * stride + peak_off + 8 + h];
+        }
+        float inverse = 1.0f / total;
+        for (int d = 0; d < 64; d++) {
+            float sum = 0.0f;
+            for (int c = 0; c < count; c++) sum += weights[c] * partials[c * stride + h * 64 + d];
+            output[h * 64 + d] = sum * inverse;
+        }
+    }
+}
+
+/* ------------------------------------------------------------------------ */
+/* Sampling: src/Needle/Ops.cs                                               */
+/* ------------------------------------------------------------------------ */
+
+/* Ops.ArgMax scalar loop (Ops.cs:1086-1089): strict >, first max wins. */
+int ndo_argmax(const float *x, int n) {
+    int best = 0;
+    for (int i = 1; i < n; i++)
+        if (x[i] > x[best]) best = i;
+    return best;
+}
+
+static int tz32(uint32_t v) { return __builtin_ctz(v); }
+
+/* Ops.ArgMaxMaskedScalar (Ops.cs:1236-1265). */
+int ndo_argmax_masked(const float *x, const uint32_t *mask, int words, int length) {
+    int best = -1;
+    float peak = -INFINITY;
+    for (int w = 0; w < words; w++) {
+        uint32_t bits = mask[w];
+        if (bits == 0) continue;
+        int bottom = w * 32;
+        if (bits == 0xFFFFFFFFu) {
+            int top = bottom + 32 <= length ? bottom + 32 : length;
+            for (int id = bottom; id < top; id++) {
+                float value = x[id];
+                if (value > peak) { peak = value; best = id; }
+            }
+            continue;
+        }
+        while (bits != 0) {
+            int id = bottom + tz32(bits);
+            bits &= bits - 1;
+            if (id >= length) continue;
+            float value = x[id];
+            if (value > peak) { peak = value; best = id; }
+        }
+    }
+    return best;
+}
+
+/* Ops.ScalarBestProbability (Ops.cs:1530-1535). */
+float ndo_best_probability(const float *values, int count, float best) {
+    float total = 0.0f;
+    for (int i = 0; i < count; i++) total += expf(values[i] - best);
+    return 1.0f / total;
+}
+
+/* Ops.ArgMaxMaskedWithProbability scalar branch (Ops.cs:1302-1330). */
+int ndo_argmax_masked_with_probability(const float *x, const uint32_t *mask, int words, int length,
+                                       float *scratch, float *probability) {
+    int best = -1, count = 0;
+    float peak = -INFINITY;
+    for (int w = 0; w < words; w++) {
+        uint32_t bits = mask[w];
+        while (bits != 0) {
+            int id = w * 32 + tz32(bits);
+            bits &= bits - 1;
+            if (id >= length) continue;
+            float value = x[id];
+            scratch[count++] = value;
+            if (value > peak) { peak = value; best = id; }
+        }
+    }
+    if (best < 0) {
+        *probability = 0.0f;
+        return -1;
+    }
+    *probability = ndo_best_probability(scratch, count, peak);
+    return best;
+}
+
+/* Ops.TopKLogSoftmax, scalar branch (Ops.cs:1092-1221): insertion top-k
+ * ordered by (value desc, index asc); log-sum-exp accumulated in double. */
+void ndo_topk_logsoftmax(const float *x, int n, int k, int *indices, float *log_probs, float *probs,
+                         int mask_special_023) {
+    float top_val[64];
+    int top_idx[64];
+    for (int i = 0; i < k; i++) { top_val[i] = -INFINITY; top_idx[i] = -1; }
+    float min_val = -INFINITY;
+    int min_idx = 0x7FFFFFFF;
+    int start = 0;
+    if (mask_special_023 && n > 1) {
+        top_val[0] = x[1];
+        top_idx[0] = 1;
+        if (k == 1) { min_val = top_val[0]; min_idx = 1; }
+        start = 4;
+    }
+    for (int i = start; i < n; i++) {
+        if (mask_special_023 && (i == 0 || i == 2 || i == 3)) continue;
+        float v = x[i];
+        if (v > min_val || (v == min_val && i < min_idx)) {
+            int pos = k - 1;
+            while (pos > 0 && (v > top_val[pos - 1] || (v == top_val[pos - 1] && i < top_idx[pos - 1]))) {
+                top_val[pos] = top_val[pos - 1];
+                top_idx[pos] = top_idx[pos - 1];
+                pos--;
+            }
+            top_val[pos] = v;
+            top_idx[pos] = i;
+            min_val = top_val[k - 1];
+            min_idx = top_idx[k - 1];
+        }
+    }
+    float peak = top_val[0];
+    double total = 0.0;
+    for (int i = 0; i < n; i++) {
+        float v = mask_special_023 && (i == 0 || i == 2 || i == 3) ? -1e30f : x[i];
+        total += exp((double)(v - peak));
+    }
+    float log_shift = peak + (float)log(total);
+    for (int m = 0; m < k; m++) {
+        indices[m] = top_idx[m];
+        float lp = top_val[m] - log_shift;
+        log_probs[m] = lp;
+        if (probs) probs[m] = expf(lp);
+    }
+}
+
+/* ------------------------------------------------------------------------ */
+/* Synthetic decoder: one row through every layer and the head.              */
+/* Structure of EngineCore.ForwardBatch/RunAttentionBatch                    */
+/* (src/Needle/Engine.cs:2303-2350, 2480-2596) with the synthetic block:     */
+/* RMSNorm -> int8 QKV -> RoPE -> int8 q / KV write -> attention -> int8 O   */
+/* -> residual; RMSNorm -> int8 gate/up -> SwiGLU -> int8 down -> residual.  */
+/* ------------------------------------------------------------------------ */
+
+int ndo_decoder_row(const ndo_decoder *m, int token, int pos, int capacity, int8_t *kv_k, int8_t *kv_v,
+                    float *kv_ks, float *kv_vs, const float *rope_cos, const float *rope_sin, float *logits) {
+    const int d = m->dim, H = m->heads, hd = m->head_dim, F = m->ffn, V = m->vocab;
+    const int width = H * hd;
+    const float inv_sqrt = 1.0f / sqrtf((float)hd);
+    size_t floats = (size_t)d * 4 + 3 * (size_t)d + 2 * (size_t)F + F + (size_t)(pos + 1) + 64;
+    float *buf = (float *)malloc(floats * sizeof(float));
+    int8_t *qbuf = (int8_t *)malloc((size_t)(F > d ? F : d) + (size_t)width);
+    if (!buf || !qbuf) {
+        free(buf);
+        free(qbuf);
+        return -1;
+    }
+    float *x = buf, *h = x + d, *o = h + d, *proj = o + d, *qkv = proj + d, *gu = qkv + 3 * d, *act = gu + 2 * F,
+          *scores = act + F;
+    int8_t *qa = qbuf, *qq = qbuf + (F > d ? F : d);
+    float qs[64];
+    for (int i = 0; i < d; i++) x[i] = ndo_half_to_single(m->embedding[(size_t)token * d + i]);
+    const int half = hd / 2;
+    for (int l = 0; l < m->layers; l++) {
+        float sa;
+        ndo_rms_norm(x, m->attn_norm[l], d, h);
+        sa = ndo_quantize_int8(h, d, qa);
+        ndo_matmul_i8g32(m->w_qkv[l], m->s_qkv[l], 3 * d, d, qa, &sa, 1, NULL, qkv, 3 * d);
+        float *q = qkv, *k = qkv + d, *v = qkv + 2 * d;
+        ndo_rope(q, H, hd, rope_cos + (size_t)pos * half, rope_sin + (size_t)pos * half);
+        ndo_rope(k, H, hd, rope_cos + (size_t)pos * half, rope_sin + (size_t)pos * half);
+        int8_t *lk = kv_k + (size_t)l * capacity * width, *lv = kv_v + (size_t)l * capacity * width;
+        float *lks = kv_ks + (size_t)l * capacity * H, *lvs = kv_vs + (size_t)l * capacity * H;
+        for (int hh = 0; hh < H; hh++) qs[hh] = ndo_quantize_int8(q + hh * hd, hd, qq + hh * hd);
+        for (int hh = 0; hh < H; hh++) {
+            lks[(size_t)pos * H + hh] = ndo_quantize_int8(k + hh * hd, hd, lk + (size_t)pos * width + hh * hd);
+            lvs[(size_t)pos * H + hh] = ndo_quantize_int8(v + hh * hd, hd, lv + (size_t)pos * width + hh * hd);
+        }
+        for (int hh = 0; hh < H; hh++)
+            ndo_attention_head(qq + hh * hd, qs[hh], lk + hh * hd, lks + hh, lv + hh * hd, lvs + hh, width, width, H, 0,
+                               pos, hd, hd, inv_sqrt, scores, o + hh * hd, NULL);
+        sa = ndo_quantize_int8(o, d, qa);
+        ndo_matmul_i8g32(m->w_o[l], m->s_o[l], d, d, qa, &sa, 1, NULL, proj, d);
+        for (int i = 0; i < d; i++) x[i] = x[i] + proj[i];
+        ndo_rms_norm(x, m->ffn_norm[l], d, h);
+        sa = ndo_quantize_int8(h, d, qa);
+        ndo_matmul_i8g32(m->w_gu[l], m->s_gu[l], 2 * F, d, qa, &sa, 1, NULL, gu, 2 * F);
+        ndo_swiglu(gu, gu + F, F, act);
+        sa = ndo_quantize_int8(act, F, qa);
+        ndo_matmul_i8g32(m->w_d[l], m->s_d[l], d, F, qa, &sa, 1, NULL, proj, d);
+        for (int i = 0; i < d; i++) x[i] = x[i] + proj[i];
+    }
+    {
+        float sa;
+        ndo_rms_norm(x, m->final_norm, d, h);
+        sa = ndo_quantize_int8(h, d, qa);
+        ndo_matmul_i8g32(m->w_head, m->s_head, V, d, qa, &sa, 1, NULL, logits, V);
+    }
+    free(buf);
+    free(qbuf);
+    return 0;
+}

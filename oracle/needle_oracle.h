@@ -1,0 +1,125 @@
+/*
+ * needle_oracle.h - CPU restatement of the needle-cs batched decode path.
+ *
+ * TEST INFRASTRUCTURE ONLY.  This library is the parity checker for the
+ * CUDA path in needle-cs_b200/.  It is imported by tests/, by
+ * __graft_entry__.smoke() and by the cpu_baseline / --impl reference legs of
+ * bench.py, and by nothing else.  The shipped library never links it.
+ *
+ * Every function restates one reference routine; the reference location is
+ * cited per function (paths are relative to the needle-cs source tree).
+ * Floating point follows the reference's scalar C# semantics: IEEE binary32,
+ * no FMA contraction (compile with -ffp-contract=off), left-to-right
+ * summation, MathF.Exp/Cos/Sin/Pow mapped to the C library's expf/cosf/sinf/
+ * powf (which is what .NET calls on Linux).
+ */
+#ifndef NEEDLE_ORACLE_H
+#define NEEDLE_ORACLE_H
+
+#include <stdint.h>
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- test-input generators (tests/Needle.Tests/Conformance/Conformance.cs:10-119) ---- */
+uint64_t ndo_xorshift_next(uint64_t *state);
+int ndo_xorshift_int(uint64_t *state, int lo, int hi);
+float ndo_xorshift_float(uint64_t *state, float scale);
+void ndo_fill_uniform(float *x, int n, uint64_t *state, float scale);
+void ndo_fill_edges(float *x, int n, uint64_t *state, float scale);
+void ndo_fill_sbyte(int8_t *x, int n, uint64_t *state, int extremes);
+void ndo_fill_bytes(uint8_t *x, int n, uint64_t *state, int extremes);
+uint16_t ndo_half_bits(float value);
+
+/* ---- row primitives (src/Needle/Scalar.cs) ---- */
+float ndo_abs_max(const float *x, int n);
+float ndo_quantize_int8(const float *x, int n, int8_t *dst);
+void ndo_quantize_rows(const float *x, int rows, int cols, int8_t *q, float *scales);
+float ndo_fake_a8(float *x, int n);
+float ndo_half_to_single(uint16_t half);
+void ndo_hadamard128(const float *src, float *dst);
+void ndo_planes(const int8_t *quantized, int bits, int8_t *dst, int *sum);
+float ndo_sigmoid(float x);
+void ndo_softmax(float *s, int n);
+void ndo_rope(float *x, int heads, int head_dim, const float *cos_t, const float *sin_t);
+void ndo_rope_tables(float theta, int qk_dim, int positions, float *cos_t, float *sin_t);
+float ndo_inverse_rms(const float *x, int n);
+void ndo_rms_norm(const float *x, const float *weight, int n, float *dst);
+void ndo_zero_centered_rms(const float *x, const float *scale, int n, float *dst);
+void ndo_swiglu(const float *gate, const float *up, int n, float *dst);
+
+/* ---- quantized matmul ---- */
+/* Codebook (src/Needle/Model.cs:36-52). */
+typedef struct {
+    float levels[16];
+    uint8_t bytes[32];
+    float byte_scale;
+} ndo_codebook;
+void ndo_codebook_fill(ndo_codebook *book, const float *levels, int count);
+
+/* CQ activations prepare, scalar branch (src/Needle/Quant.cs:471-484). */
+void ndo_prepare_cq(const float *x, int tokens, int cols, int bits, int8_t *values, float *scales,
+                    float *offsets, int stride);
+/* CQ MatMulRows (src/Needle/Scalar.cs:146-192). */
+void ndo_matmul_rows_cq(const uint8_t *indices, const uint16_t *norms, const ndo_codebook *book, int rows,
+                        int cols, int bits, const int8_t *values, const float *scales, const float *offsets,
+                        int stride, int tokens, float *y, int ldy, int row_start, int row_end);
+/* I8G32: int8 weights [N][K], fp16 scale per (row, 32-column group).  Same
+ * skeleton as Scalar.MatMulRows with a 32-group and raw int8 weights:
+ *   D[t][n][g] = sum_{k in g} w[n][k] * q[t][k]              (int32)
+ *   y[t][n]    = sum_g (half(sw[n][g]) * sa[t]) * (float)D     (fp32, g ascending)
+ * acc (nullable) receives D as [M][N][K/32]. */
+void ndo_matmul_i8g32(const int8_t *w, const uint16_t *sw, int n_rows, int k, const int8_t *q, const float *sa,
+                      int m, int32_t *acc, float *y, int ldy);
+
+/* ---- attention ---- */
+/* Scalar.AttentionHead (src/Needle/Scalar.cs:290-312) with qk/v widths as
+ * parameters; inv_sqrt_dim replaces the hard-coded 1/sqrt(48). */
+void ndo_attention_head(const int8_t *query, float query_scale, const int8_t *keys, const float *key_scales,
+                        const int8_t *values, const float *value_scales, int key_stride, int value_stride,
+                        int scale_stride, int first, int last, int qk_dim, int v_dim, float inv_sqrt_dim,
+                        float *scores, float *output, float *probabilities);
+/* Attention.MergePartials scalar branch (src/Needle/Blocks.cs:750-817):
+ * partial c = {out[heads*64] at c*stride, peak[h] at c*stride+peak_off,
+ * sum[h] at c*stride+peak_off+8}. */
+void ndo_merge_partials(const float *partials, int count, int heads, int stride, int peak_off, float *output);
+
+/* ---- sampling ---- */
+int ndo_argmax(const float *x, int n);                                       /* Ops.cs:1052-1090 scalar tail */
+int ndo_argmax_masked(const float *x, const uint32_t *mask, int words, int length); /* Ops.cs:1236-1265 */
+float ndo_best_probability(const float *values, int count, float best);      /* Ops.cs:1530-1535 */
+int ndo_argmax_masked_with_probability(const float *x, const uint32_t *mask, int words, int length,
+                                       float *scratch, float *probability);  /* Ops.cs:1302-1330 */
+void ndo_topk_logsoftmax(const float *x, int n, int k, int *indices, float *log_probs, float *probs,
+                         int mask_special_023);                              /* Ops.cs:1092-1221 */
+
+/* ---- synthetic decoder step ---- */
+typedef struct {
+    int layers, dim, heads, head_dim, ffn, vocab;
+    float rope_theta, eps;
+    /* per layer l (arrays of length layers): */
+    const int8_t **w_qkv;  const uint16_t **s_qkv;   /* [3*dim][dim]      */
+    const int8_t **w_o;    const uint16_t **s_o;     /* [dim][dim]        */
+    const int8_t **w_gu;   const uint16_t **s_gu;    /* [2*ffn][dim]      */
+    const int8_t **w_d;    const uint16_t **s_d;     /* [dim][ffn]        */
+    const float **attn_norm, **ffn_norm;             /* [dim]             */
+    const float *final_norm;                         /* [dim]             */
+    const uint16_t *embedding;                       /* fp16 [vocab][dim] */
+    const int8_t *w_head; const uint16_t *s_head;    /* [vocab][dim]      */
+} ndo_decoder;
+
+/* One decoder layer stack + head for one row at absolute position `pos`.
+ * kv_k/kv_v: int8 [layers][capacity][heads*head_dim]; kv_ks/kv_vs: fp32
+ * [layers][capacity][heads] (the reference slot layout,
+ * src/Needle/Engine.cs:184-187,220-223). Positions [0,pos) must be filled;
+ * this call writes position pos (KV write, src/Needle/Engine.cs:2552-2569)
+ * and writes logits [vocab]. Returns 0, or -1 if scratch allocation failed. */
+int ndo_decoder_row(const ndo_decoder *m, int token, int pos, int capacity, int8_t *kv_k, int8_t *kv_v,
+                    float *kv_ks, float *kv_vs, const float *rope_cos, const float *rope_sin, float *logits);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

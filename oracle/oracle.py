@@ -1,0 +1,217 @@
+"""ctypes wrapper of the CPU parity oracle (oracle/build/liboracle.so).
+
+TEST INFRASTRUCTURE ONLY.  Imported by tests/, __graft_entry__.smoke() and
+the CPU-baseline legs of bench.py as the checker; never by the library.
+"""
+import ctypes
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "build", "liboracle.so")
+
+_c = ctypes
+P = _c.c_void_p
+I = _c.c_int
+F = _c.c_float
+U64 = _c.c_uint64
+PU64 = _c.POINTER(_c.c_uint64)
+
+_SIGS = {
+    "ndo_xorshift_next": (U64, [PU64]),
+    "ndo_xorshift_int": (I, [PU64, I, I]),
+    "ndo_xorshift_float": (F, [PU64, F]),
+    "ndo_fill_uniform": (None, [P, I, PU64, F]),
+    "ndo_fill_edges": (None, [P, I, PU64, F]),
+    "ndo_fill_sbyte": (None, [P, I, PU64, I]),
+    "ndo_fill_bytes": (None, [P, I, PU64, I]),
+    "ndo_half_bits": (_c.c_uint16, [F]),
+    "ndo_abs_max": (F, [P, I]),
+    "ndo_quantize_int8": (F, [P, I, P]),
+    "ndo_quantize_rows": (None, [P, I, I, P, P]),
+    "ndo_fake_a8": (F, [P, I]),
+    "ndo_half_to_single": (F, [_c.c_uint16]),
+    "ndo_hadamard128": (None, [P, P]),
+    "ndo_planes": (None, [P, I, P, _c.POINTER(I)]),
+    "ndo_sigmoid": (F, [F]),
+    "ndo_softmax": (None, [P, I]),
+    "ndo_rope": (None, [P, I, I, P, P]),
+    "ndo_rope_tables": (None, [F, I, I, P, P]),
+    "ndo_inverse_rms": (F, [P, I]),
+    "ndo_rms_norm": (None, [P, P, I, P]),
+    "ndo_zero_centered_rms": (None, [P, P, I, P]),
+    "ndo_swiglu": (None, [P, P, I, P]),
+    "ndo_codebook_fill": (None, [P, P, I]),
+    "ndo_prepare_cq": (None, [P, I, I, I, P, P, P, I]),
+    "ndo_matmul_rows_cq": (None, [P, P, P, I, I, I, P, P, P, I, I, P, I, I, I]),
+    "ndo_matmul_i8g32": (None, [P, P, I, I, P, P, I, P, P, I]),
+    "ndo_attention_head": (None, [P, F, P, P, P, P, I, I, I, I, I, I, I, F, P, P, P]),
+    "ndo_merge_partials": (None, [P, I, I, I, I, P]),
+    "ndo_argmax": (I, [P, I]),
+    "ndo_argmax_masked": (I, [P, P, I, I]),
+    "ndo_best_probability": (F, [P, I, F]),
+    "ndo_argmax_masked_with_probability": (I, [P, P, I, I, P, _c.POINTER(F)]),
+    "ndo_topk_logsoftmax": (None, [P, I, I, P, P, P, I]),
+    "ndo_decoder_row": (I, [P, I, I, I, P, P, P, P, P, P, P]),
+}
+
+_lib = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(f"oracle not built: {LIB_PATH} (run make -C oracle)")
+        h = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in _SIGS.items():
+            fn = getattr(h, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = h
+    return _lib
+
+
+def ptr(a):
+    return None if a is None else a.ctypes.data
+
+
+class XorShift64:
+    """Port of the reference test RNG (Conformance.cs:10-38), state in C."""
+
+    def __init__(self, seed):
+        self.state = _c.c_uint64(seed if seed != 0 else 0x9E3779B97F4A7C15)
+
+    def next(self):
+        return lib().ndo_xorshift_next(_c.byref(self.state))
+
+    def next_int(self, lo, hi):
+        return lib().ndo_xorshift_int(_c.byref(self.state), lo, hi)
+
+    def next_float(self, scale):
+        return lib().ndo_xorshift_float(_c.byref(self.state), scale)
+
+    def fill_edges(self, n, scale):
+        x = np.empty(max(n, 1), np.float32)
+        lib().ndo_fill_edges(ptr(x), max(n, 1), _c.byref(self.state), scale)
+        return x
+
+    def fill_uniform(self, n, scale):
+        x = np.empty(max(n, 1), np.float32)
+        lib().ndo_fill_uniform(ptr(x), max(n, 1), _c.byref(self.state), scale)
+        return x
+
+    def fill_sbyte(self, n, extremes):
+        x = np.empty(max(n, 1), np.int8)
+        lib().ndo_fill_sbyte(ptr(x), max(n, 1), _c.byref(self.state), int(extremes))
+        return x
+
+    def fill_bytes(self, n, extremes):
+        x = np.empty(max(n, 1), np.uint8)
+        lib().ndo_fill_bytes(ptr(x), max(n, 1), _c.byref(self.state), int(extremes))
+        return x
+
+
+def f32(a):
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def quantize_int8(x):
+    x = f32(x)
+    q = np.empty(x.size, np.int8)
+    s = lib().ndo_quantize_int8(ptr(x), x.size, ptr(q))
+    return q, s
+
+
+def quantize_rows(x):
+    x = f32(x)
+    rows, cols = x.shape
+    q = np.empty((rows, cols), np.int8)
+    s = np.empty(rows, np.float32)
+    lib().ndo_quantize_rows(ptr(x), rows, cols, ptr(q), ptr(s))
+    return q, s
+
+
+def matmul_i8g32(q, sa, w, sw, want_acc=False):
+    q = np.ascontiguousarray(q, np.int8)
+    sa = f32(sa)
+    w = np.ascontiguousarray(w, np.int8)
+    sw = np.ascontiguousarray(sw, np.uint16)
+    m, k = q.shape
+    n = w.shape[0]
+    y = np.empty((m, n), np.float32)
+    acc = np.empty((m, n, k // 32), np.int32) if want_acc else None
+    lib().ndo_matmul_i8g32(ptr(w), ptr(sw), n, k, ptr(q), ptr(sa), m, ptr(acc), ptr(y), n)
+    return (y, acc) if want_acc else y
+
+
+def rms_norm(x, w):
+    x = f32(x)
+    w = f32(w)
+    out = np.empty_like(x)
+    for r in range(x.shape[0]):
+        lib().ndo_rms_norm(ptr(x[r]), ptr(w), x.shape[1], ptr(out[r]))
+    return out
+
+
+def softmax(s):
+    s = f32(s).copy()
+    lib().ndo_softmax(ptr(s), s.size)
+    return s
+
+
+def argmax_masked(x, mask, length):
+    x = f32(x)
+    mask = np.ascontiguousarray(mask, np.uint32)
+    return lib().ndo_argmax_masked(ptr(x), ptr(mask), mask.size, length)
+
+
+def best_probability(values, best):
+    values = f32(values)
+    return lib().ndo_best_probability(ptr(values), values.size, best)
+
+
+def argmax_masked_with_probability(x, mask, length):
+    x = f32(x)
+    mask = np.ascontiguousarray(mask, np.uint32)
+    scratch = np.empty(max(x.size, 1), np.float32)
+    p = _c.c_float()
+    best = lib().ndo_argmax_masked_with_probability(ptr(x), ptr(mask), mask.size, length, ptr(scratch),
+                                                    _c.byref(p))
+    return best, p.value
+
+
+def topk_logsoftmax(x, k, mask_special_023=False, want_probs=True):
+    x = f32(x)
+    idx = np.empty(k, np.int32)
+    lp = np.empty(k, np.float32)
+    pr = np.empty(k, np.float32) if want_probs else None
+    lib().ndo_topk_logsoftmax(ptr(x), x.size, k, ptr(idx), ptr(lp), ptr(pr), int(mask_special_023))
+    return idx, lp, pr
+
+
+def attention_head(query, query_scale, keys, key_scales, values, value_scales, key_stride, value_stride,
+                   scale_stride, first, last, qk_dim, v_dim, inv_sqrt_dim, probabilities=None):
+    count = last - first + 1
+    scores = np.empty(max(count, 1) + 8, np.float32)
+    out = np.empty(v_dim, np.float32)
+    lib().ndo_attention_head(ptr(query), query_scale, ptr(keys), ptr(key_scales), ptr(values), ptr(value_scales),
+                             key_stride, value_stride, scale_stride, first, last, qk_dim, v_dim, inv_sqrt_dim,
+                             ptr(scores), ptr(out), ptr(probabilities))
+    return out
+
+
+def merge_partials(partials, count, heads, stride, peak_off):
+    partials = f32(partials)
+    out = np.empty(heads * 64, np.float32)
+    lib().ndo_merge_partials(ptr(partials), count, heads, stride, peak_off, ptr(out))
+    return out
+
+
+def rope_tables(theta, qk_dim, positions):
+    half = qk_dim // 2
+    c = np.empty((positions, half), np.float32)
+    s = np.empty((positions, half), np.float32)
+    lib().ndo_rope_tables(theta, qk_dim, positions, ptr(c), ptr(s))
+    return c, s
