@@ -49,19 +49,17 @@ class ClockSampler:
         self.lines = []
 
     def __enter__(self):
+        import tempfile
+
+        self.path = tempfile.mktemp(prefix="ndl_clocks_", suffix=".csv")
         try:
+            self.file = open(self.path, "w")
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits", "-lms", "100",
-                 "-i", str(self.device_index)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._drain, daemon=True)
-            self.thread.start()
+                 "-i", str(self.device_index)], stdout=self.file, stderr=subprocess.DEVNULL, text=True)
         except Exception:
             self.proc = None
         return self
-
-    def _drain(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
 
     def __exit__(self, *exc):
         if self.proc is not None:
@@ -70,6 +68,13 @@ class ClockSampler:
                 self.proc.wait(timeout=5)
             except Exception:
                 self.proc.kill()
+            self.file.close()
+            try:
+                with open(self.path) as f:
+                    self.lines = [ln.strip() for ln in f if ln.strip()]
+                os.unlink(self.path)
+            except OSError:
+                pass
 
     def summary(self):
         sm, mx, reasons = [], None, set()

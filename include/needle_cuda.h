@@ -137,6 +137,78 @@ NDL_API int ndl_matmul_i8g32_batched(const int8_t *q, const float *sa, int m, co
                                      const uint16_t *sw, int n, int k, int batch, long long w_stride,
                                      long long sw_stride, float *y, int ldy, long long y_stride, void *stream);
 
+/* ------------------------------------------------------------------ */
+/* Batched decode engine (replaces BatchedEngine + EngineCore slots)   */
+/* ------------------------------------------------------------------ */
+typedef struct ndl_engine ndl_engine;
+
+/* Synthetic decoder (I8G32 weights generated on the device from `seed`):
+ * RMSNorm -> int8 QKV -> RoPE -> paged int8 KV -> attention -> int8 O ->
+ * residual; RMSNorm -> int8 gate|up -> SwiGLU -> int8 down -> residual;
+ * final RMSNorm -> int8 head quantized from the fp16 embedding. */
+typedef struct {
+    int layers, dim, heads, head_dim, ffn, vocab;
+    float rope_theta; /* <= 0 selects 10000 */
+    uint64_t seed;
+} ndl_decoder_config;
+
+typedef struct {
+    int device;
+    int slots;     /* resident sessions (BatchedEngine slots, src/Needle/BatchEngine.cs:9-14) */
+    int capacity;  /* positions per slot, a multiple of 64 */
+    int kv_pages;  /* page pool size, 0 = slots * capacity / 64 */
+    int max_rows;  /* rows per forward_batch */
+    int max_heads; /* logits rows per forward_batch */
+} ndl_engine_config;
+
+/* Creates an engine on `device` and generates the synthetic decoder there
+ * (Model.Open + new BatchedEngine, src/Needle/Model.cs:400-425,
+ * src/Needle/BatchEngine.cs:9-14). */
+NDL_API int ndl_engine_create(const ndl_engine_config *engine, const ndl_decoder_config *model, ndl_engine **out);
+NDL_API int ndl_engine_destroy(ndl_engine *e);
+/* The engine's CUDA stream (cudaStream_t as void*). */
+NDL_API int ndl_engine_stream(ndl_engine *e, void **stream);
+/* Device view of a named tensor (layer >= 0 for per-layer tensors): weights
+ * w_qkv s_qkv w_o s_o w_gu s_gu w_d s_d attn_norm ffn_norm; global
+ * final_norm embedding w_head s_head rope_cos rope_sin kv_pool page_table
+ * logits.  For export and tests; the pointer stays owned by the engine. */
+NDL_API int ndl_engine_tensor(ndl_engine *e, const char *name, int layer, void **ptr, size_t *bytes);
+/* Synchronous host copy of the first `bytes` bytes of a named tensor. */
+NDL_API int ndl_engine_read_tensor(ndl_engine *e, const char *name, int layer, void *host, size_t bytes);
+NDL_API int ndl_engine_page_bytes(ndl_engine *e, size_t *bytes);
+/* Waits for the engine stream and reports kernel-side status (bounds,
+ * timeouts) as NDL_ERR_BOUNDS / NDL_ERR_TIMEOUT. */
+NDL_API int ndl_engine_sync(ndl_engine *e);
+
+/* Slot state: BatchedEngine.SlotLength/ResetSlot/MarkSlot/RewindSlot
+ * (src/Needle/BatchEngine.cs:23-30 -> src/Needle/Engine.cs:2261-2283). */
+NDL_API int ndl_slot_length(ndl_engine *e, int slot, int *length);
+NDL_API int ndl_slot_reset(ndl_engine *e, int slot);
+NDL_API int ndl_slot_mark(ndl_engine *e, int slot);
+NDL_API int ndl_slot_rewind(ndl_engine *e, int slot);
+/* Page id backing positions [64*index, 64*index+64) of a slot (-1 = none). */
+NDL_API int ndl_slot_page(ndl_engine *e, int slot, int index, int *page);
+/* Appends `count` synthetic prefix positions to a slot: K/V fp16 N(0,1)
+ * from (seed, session) quantized per (position, head) on load. */
+NDL_API int ndl_slot_fill_synthetic(ndl_engine *e, int slot, int count, uint64_t seed, uint64_t session);
+
+/* One batched step: EngineCore.ForwardBatch (src/Needle/Engine.cs:2303-2350)
+ * via BatchedEngine.ForwardBatch (src/Needle/BatchEngine.cs:34).  Host
+ * arrays.  Consecutive rows of one slot form a prefill run; logits are
+ * computed for head_rows only (compact order).  Asynchronous on the engine
+ * stream; NDL_FAIL_CONTEXT_EXHAUSTED when a slot would exceed capacity. */
+NDL_API int ndl_forward_batch(ndl_engine *e, const int *tokens, const int *row_slots, int rows, const int *head_rows,
+                              int heads);
+/* BatchedEngine.BatchLogitsRow (src/Needle/BatchEngine.cs:37): host copy. */
+NDL_API int ndl_batch_logits_row(ndl_engine *e, int compact_row, float *out);
+/* Masked greedy selection on every head row of the last step
+ * (Ops.ArgMaxMasked / ArgMaxMaskedWithProbability, src/Needle/Ops.cs:1223-1330).
+ * masks: host [heads][words] uint32 (NULL = all allowed); probs nullable. */
+NDL_API int ndl_sample_argmax(ndl_engine *e, const uint32_t *masks, int words, int *ids, float *probs);
+/* Beam expansion (Ops.TopKLogSoftmax, src/Needle/Ops.cs:1092-1221) on every
+ * head row: ids/log_probs/probs [heads][k], k <= 8; probs nullable. */
+NDL_API int ndl_sample_topk(ndl_engine *e, int k, int mask_special_023, int *ids, float *log_probs, float *probs);
+
 #ifdef __cplusplus
 }
 #endif

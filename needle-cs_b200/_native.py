@@ -35,7 +35,36 @@ SIGNATURES = {
                                  c_void_p, c_void_p, c_void_p]),
     "ndl_matmul_i8g32_batched": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_int, c_int, c_int, c_ll,
                                          c_ll, c_void_p, c_int, c_ll, c_void_p]),
+    "ndl_engine_create": (c_int, [c_void_p, c_void_p, ctypes.POINTER(c_void_p)]),
+    "ndl_engine_destroy": (c_int, [c_void_p]),
+    "ndl_engine_stream": (c_int, [c_void_p, ctypes.POINTER(c_void_p)]),
+    "ndl_engine_tensor": (c_int, [c_void_p, c_char_p, c_int, ctypes.POINTER(c_void_p), ctypes.POINTER(c_size_t)]),
+    "ndl_engine_read_tensor": (c_int, [c_void_p, c_char_p, c_int, c_void_p, c_size_t]),
+    "ndl_engine_page_bytes": (c_int, [c_void_p, ctypes.POINTER(c_size_t)]),
+    "ndl_engine_sync": (c_int, [c_void_p]),
+    "ndl_slot_length": (c_int, [c_void_p, c_int, ctypes.POINTER(c_int)]),
+    "ndl_slot_reset": (c_int, [c_void_p, c_int]),
+    "ndl_slot_mark": (c_int, [c_void_p, c_int]),
+    "ndl_slot_rewind": (c_int, [c_void_p, c_int]),
+    "ndl_slot_page": (c_int, [c_void_p, c_int, c_int, ctypes.POINTER(c_int)]),
+    "ndl_slot_fill_synthetic": (c_int, [c_void_p, c_int, c_int, c_u64, c_u64]),
+    "ndl_forward_batch": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int]),
+    "ndl_batch_logits_row": (c_int, [c_void_p, c_int, c_void_p]),
+    "ndl_sample_argmax": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p]),
+    "ndl_sample_topk": (c_int, [c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p]),
 }
+
+
+class DecoderConfig(ctypes.Structure):
+    """ndl_decoder_config."""
+    _fields_ = [("layers", c_int), ("dim", c_int), ("heads", c_int), ("head_dim", c_int), ("ffn", c_int),
+                ("vocab", c_int), ("rope_theta", c_float), ("seed", c_u64)]
+
+
+class EngineConfig(ctypes.Structure):
+    """ndl_engine_config."""
+    _fields_ = [("device", c_int), ("slots", c_int), ("capacity", c_int), ("kv_pages", c_int), ("max_rows", c_int),
+                ("max_heads", c_int)]
 
 
 class NeedleError(RuntimeError):

@@ -3,6 +3,7 @@
 // PTX wrappers.  Everything here is used by host and device code alike.
 #pragma once
 
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -50,6 +51,18 @@ __host__ __device__ __forceinline__ float half_to_float_ref(uint16_t half) {
     return f;
 #endif
 }
+
+#ifdef __CUDACC__
+// Same values as half_to_float_ref with one hardware conversion: IEEE
+// binary16 decode is identical for finite halves; the reference's Inf/NaN
+// pattern (no special case) is patched in with a select.
+__device__ __forceinline__ float half_to_float_ref_fast(uint16_t h) {
+    float f = __half2float(__ushort_as_half(h));
+    if ((h & 0x7C00u) == 0x7C00u)
+        f = __uint_as_float(((((uint32_t)h & 0x7FFFu) << 13) + 0x38000000u) | ((uint32_t)(h & 0x8000u) << 16));
+    return f;
+}
+#endif
 
 // IEEE round-to-nearest-even float -> binary16 (integer-only).
 __host__ __device__ __forceinline__ uint16_t float_to_half_rne(float f) {

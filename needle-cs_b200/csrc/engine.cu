@@ -1,0 +1,664 @@
+// Batched decode engine: the B200 replacement of BatchedEngine / EngineCore
+// (src/Needle/BatchEngine.cs:5-50, src/Needle/Engine.cs:2255-2350).
+//
+// Owns the device weights of the synthetic decoder, the paged int8 KV pool,
+// per-slot lengths / marks / page tables, and the step buffers.  One host
+// thread per engine; all device work is ordered on the engine's stream.
+//
+// forward_batch(tokens, row_slots, rows, head_rows, heads) follows the
+// reference's ForwardBatch contract: consecutive rows of one slot are a
+// prefill run at positions len, len+1, ...; every row attends causally to
+// its own slot; logits are produced only for head_rows (compact order).
+#include <stdio.h>
+#include <string.h>
+
+#include <algorithm>
+#include <cmath>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "kernels.cuh"
+#include "kv.cuh"
+
+namespace ndl {
+
+int launch_step_prepare(const int32_t *updates, int n_updates, int32_t *page_table, int max_pages,
+                        const int32_t *tokens, int rows, const uint16_t *embedding, int vocab, int dim, float *x,
+                        int *status, cudaStream_t stream);
+int launch_swiglu_quantize(const float *gu, int rows, int ffn, float *act, int8_t *q, float *scales,
+                           cudaStream_t stream);
+int launch_gather_rows(const float *x, const int32_t *idx, int n, int dim, float *out, cudaStream_t stream);
+int launch_argmax_masked(const float *x, long long ldx, const uint32_t *mask, int words, long long ldm, int length,
+                         int rows, int32_t *ids, float *probs, cudaStream_t stream);
+int launch_topk_logsoftmax(const float *x, long long ldx, int n, int k, int mask023, int rows, int32_t *idx,
+                           float *logp, float *probs, cudaStream_t stream);
+int launch_kv_fill(uint64_t seed, uint64_t session, int layers, int heads, int first, int count,
+                   const int32_t *page_row, uint8_t *pool, long long page_bytes, cudaStream_t stream);
+
+// Stream ids of the synthetic decoder tensors under the model seed.
+enum : uint64_t {
+    kStreamEmbedding = 1,
+    kStreamFinalNorm = 2,
+    kStreamLayerBase = 100,  // + 16 * layer + field
+};
+constexpr int kAttnChunkPages = 2;  // pages per attention work item
+enum : int { kFQkvW, kFQkvS, kFOW, kFOS, kFGuW, kFGuS, kFDW, kFDS, kFAttnNorm, kFFfnNorm };
+
+struct DeviceLayer {
+    int8_t *w_qkv, *w_o, *w_gu, *w_d;
+    uint16_t *s_qkv, *s_o, *s_gu, *s_d;
+    float *attn_norm, *ffn_norm;
+};
+
+}  // namespace ndl
+
+struct ndl_engine {
+    ndl_engine_config ec{};
+    ndl_decoder_config dc{};
+    cudaStream_t stream = nullptr;
+    bool own_stream = false;
+    std::vector<void *> allocations;
+    std::vector<ndl::DeviceLayer> layers;
+    float *final_norm = nullptr;
+    uint16_t *embedding = nullptr;
+    int8_t *w_head = nullptr;
+    uint16_t *s_head = nullptr;
+    float *rope_cos = nullptr, *rope_sin = nullptr;
+    // KV
+    int max_pages = 0;
+    size_t page_bytes = 0;
+    uint8_t *pool = nullptr;
+    int32_t *d_page_table = nullptr;
+    std::vector<int32_t> page_table;  // host mirror [slots][max_pages]
+    std::vector<int32_t> free_pages;
+    std::vector<int> slot_len, slot_mark;
+    // step buffers
+    float *x = nullptr, *qkv = nullptr, *attn = nullptr, *gu = nullptr, *act = nullptr, *head_x = nullptr;
+    int8_t *qa = nullptr, *q8 = nullptr;
+    float *sa = nullptr, *qs = nullptr;
+    float *logits = nullptr;
+    int32_t *d_meta = nullptr;
+    int32_t *h_meta = nullptr;  // pinned staging
+    size_t meta_ints = 0;
+    float *partials = nullptr;
+    int *arrivals = nullptr;
+    int *d_status = nullptr;
+    int32_t *d_ids = nullptr;
+    float *d_probs = nullptr, *d_logp = nullptr;
+    uint32_t *d_masks = nullptr;
+    void *h_out = nullptr;  // pinned sampling results
+    int last_rows = 0, last_heads = 0;
+    int max_chunks_cap = 0;
+    // offsets of the last step's metadata in d_meta
+    int off_tokens = 0, off_slot = 0, off_pos = 0, off_order = 0, off_head = 0, off_updates = 0;
+};
+
+using namespace ndl;
+
+namespace {
+
+template <typename T>
+int dalloc(ndl_engine *e, T **p, size_t count) {
+    void *ptr = nullptr;
+    cudaError_t err = cudaMalloc(&ptr, count * sizeof(T) > 0 ? count * sizeof(T) : 16);
+    if (err != cudaSuccess) {
+        cudaGetLastError();
+        return set_error(NDL_ERR_OUT_OF_MEMORY, "cudaMalloc(%zu): %s", count * sizeof(T), cudaGetErrorString(err));
+    }
+    e->allocations.push_back(ptr);
+    *p = static_cast<T *>(ptr);
+    return NDL_OK;
+}
+
+#define TRY(x)                         \
+    do {                               \
+        int st_ = (x);                 \
+        if (st_ != NDL_OK) return st_; \
+    } while (0)
+
+uint64_t layer_stream(int layer, int field) { return kStreamLayerBase + 16ull * layer + field; }
+
+// Norm weights: 1 + 0.1 * normal (host, exact float ops).
+void norm_values(uint64_t seed, uint64_t stream, int n, std::vector<float> &out) {
+    out.resize(n);
+    uint64_t key = synth_key(seed, stream);
+    for (int i = 0; i < n; i++) {
+        float z = synth_normal(key, i);
+        float t = 0.1f * z;
+        out[i] = 1.0f + t;
+    }
+}
+
+int upload(ndl_engine *e, void *dst, const void *src, size_t bytes) {
+    NDL_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, e->stream));
+    NDL_CUDA(cudaStreamSynchronize(e->stream));
+    return NDL_OK;
+}
+
+// LM head quantized from the fp16 embedding per (row, 32-group):
+// s = fp16(max|e| / 127) (1 if the group is zero), w = clamp(rint(e * (1/float(s))), -127, 127).
+void quantize_head(const std::vector<uint16_t> &emb, int vocab, int dim, std::vector<int8_t> &w,
+                   std::vector<uint16_t> &s) {
+    int G = dim / 32;
+    w.resize((size_t)vocab * dim);
+    s.resize((size_t)vocab * G);
+    for (int r = 0; r < vocab; r++)
+        for (int g = 0; g < G; g++) {
+            const uint16_t *e = emb.data() + (size_t)r * dim + g * 32;
+            float peak = 0.0f;
+            for (int i = 0; i < 32; i++) peak = std::max(peak, std::fabs(half_to_float_ref(e[i])));
+            uint16_t sh = peak > 0.0f ? float_to_half_rne(peak / 127.0f) : float_to_half_rne(1.0f);
+            float sf = half_to_float_ref(sh);
+            float inv = 1.0f / sf;
+            s[(size_t)r * G + g] = sh;
+            for (int i = 0; i < 32; i++) {
+                float v = std::nearbyint(half_to_float_ref(e[i]) * inv);
+                v = std::min(std::max(v, -127.0f), 127.0f);
+                w[(size_t)r * dim + g * 32 + i] = (int8_t)v;
+            }
+        }
+}
+
+int build_weights(ndl_engine *e) {
+    const ndl_decoder_config &c = e->dc;
+    const int d = c.dim, F = c.ffn, V = c.vocab, G = d / 32, GF = F / 32;
+    const uint64_t seed = c.seed;
+    e->layers.resize(c.layers);
+    std::vector<float> host;
+    for (int l = 0; l < c.layers; l++) {
+        DeviceLayer &L = e->layers[l];
+        TRY(dalloc(e, &L.w_qkv, (size_t)3 * d * d));
+        TRY(dalloc(e, &L.s_qkv, (size_t)3 * d * G));
+        TRY(dalloc(e, &L.w_o, (size_t)d * d));
+        TRY(dalloc(e, &L.s_o, (size_t)d * G));
+        TRY(dalloc(e, &L.w_gu, (size_t)2 * F * d));
+        TRY(dalloc(e, &L.s_gu, (size_t)2 * F * G));
+        TRY(dalloc(e, &L.w_d, (size_t)d * F));
+        TRY(dalloc(e, &L.s_d, (size_t)d * GF));
+        TRY(dalloc(e, &L.attn_norm, d));
+        TRY(dalloc(e, &L.ffn_norm, d));
+        cudaStream_t s = e->stream;
+        TRY(ndl_synth_int8_device(seed, layer_stream(l, kFQkvW), 0, (size_t)3 * d * d, L.w_qkv, s));
+        TRY(ndl_synth_uniform_f16_device(seed, layer_stream(l, kFQkvS), 0, (size_t)3 * d * G, 0.001f, 0.02f,
+                                         L.s_qkv, s));
+        TRY(ndl_synth_int8_device(seed, layer_stream(l, kFOW), 0, (size_t)d * d, L.w_o, s));
+        TRY(ndl_synth_uniform_f16_device(seed, layer_stream(l, kFOS), 0, (size_t)d * G, 0.001f, 0.02f, L.s_o, s));
+        TRY(ndl_synth_int8_device(seed, layer_stream(l, kFGuW), 0, (size_t)2 * F * d, L.w_gu, s));
+        TRY(ndl_synth_uniform_f16_device(seed, layer_stream(l, kFGuS), 0, (size_t)2 * F * G, 0.001f, 0.02f,
+                                         L.s_gu, s));
+        TRY(ndl_synth_int8_device(seed, layer_stream(l, kFDW), 0, (size_t)d * F, L.w_d, s));
+        TRY(ndl_synth_uniform_f16_device(seed, layer_stream(l, kFDS), 0, (size_t)d * GF, 0.001f, 0.02f, L.s_d, s));
+        norm_values(seed, layer_stream(l, kFAttnNorm), d, host);
+        TRY(upload(e, L.attn_norm, host.data(), d * sizeof(float)));
+        norm_values(seed, layer_stream(l, kFFfnNorm), d, host);
+        TRY(upload(e, L.ffn_norm, host.data(), d * sizeof(float)));
+    }
+    TRY(dalloc(e, &e->final_norm, d));
+    norm_values(seed, kStreamFinalNorm, d, host);
+    TRY(upload(e, e->final_norm, host.data(), d * sizeof(float)));
+    // embedding fp16 N(0, 0.02) and the int8 head quantized from it
+    std::vector<uint16_t> emb((size_t)V * d);
+    ndl_synth_normal_f16(seed, kStreamEmbedding, 0, emb.size(), 0.02f, emb.data());
+    std::vector<int8_t> wh;
+    std::vector<uint16_t> sh;
+    quantize_head(emb, V, d, wh, sh);
+    TRY(dalloc(e, &e->embedding, emb.size()));
+    TRY(dalloc(e, &e->w_head, wh.size()));
+    TRY(dalloc(e, &e->s_head, sh.size()));
+    TRY(upload(e, e->embedding, emb.data(), emb.size() * 2));
+    TRY(upload(e, e->w_head, wh.data(), wh.size()));
+    TRY(upload(e, e->s_head, sh.data(), sh.size() * 2));
+    // RoPE tables (EngineCore.RopeFrequencies/BuildRopeTables, src/Needle/Engine.cs:336-356)
+    const int half = c.head_dim / 2, cap = e->ec.capacity;
+    std::vector<float> freq(half), cs((size_t)cap * half), sn((size_t)cap * half);
+    for (int i = 0; i < half; i++) freq[i] = 1.0f / powf(c.rope_theta, 2.0f * (float)i / (float)c.head_dim);
+    for (int p = 0; p < cap; p++)
+        for (int i = 0; i < half; i++) {
+            float angle = (float)p * freq[i];
+            cs[(size_t)p * half + i] = cosf(angle);
+            sn[(size_t)p * half + i] = sinf(angle);
+        }
+    TRY(dalloc(e, &e->rope_cos, cs.size()));
+    TRY(dalloc(e, &e->rope_sin, sn.size()));
+    TRY(upload(e, e->rope_cos, cs.data(), cs.size() * 4));
+    TRY(upload(e, e->rope_sin, sn.data(), sn.size() * 4));
+    NDL_CUDA(cudaStreamSynchronize(e->stream));
+    return NDL_OK;
+}
+
+int build_buffers(ndl_engine *e) {
+    const ndl_decoder_config &c = e->dc;
+    const int R = e->ec.max_rows, Hd = e->ec.max_heads, d = c.dim, F = c.ffn;
+    TRY(dalloc(e, &e->x, (size_t)R * d));
+    TRY(dalloc(e, &e->qkv, (size_t)R * 3 * d));
+    TRY(dalloc(e, &e->attn, (size_t)R * d));
+    TRY(dalloc(e, &e->gu, (size_t)R * 2 * F));
+    TRY(dalloc(e, &e->act, (size_t)R * F));
+    TRY(dalloc(e, &e->head_x, (size_t)Hd * d));
+    TRY(dalloc(e, &e->qa, (size_t)R * std::max(d, F)));
+    TRY(dalloc(e, &e->q8, (size_t)R * d));
+    TRY(dalloc(e, &e->sa, (size_t)R));
+    TRY(dalloc(e, &e->qs, (size_t)R * c.heads));
+    TRY(dalloc(e, &e->logits, (size_t)Hd * c.vocab));
+    e->max_chunks_cap = e->max_pages;  // chunk_pages >= 1
+    TRY(dalloc(e, &e->partials, (size_t)R * c.heads * e->max_chunks_cap * kPartialFloats));
+    TRY(dalloc(e, &e->arrivals, (size_t)R * c.heads));
+    NDL_CUDA(cudaMemsetAsync(e->arrivals, 0, (size_t)R * c.heads * sizeof(int), e->stream));
+    TRY(dalloc(e, &e->d_status, 1));
+    NDL_CUDA(cudaMemsetAsync(e->d_status, 0, sizeof(int), e->stream));
+    // metadata: tokens, slots, positions, order (R each) + head rows (Hd) + updates (3 per row + slack)
+    e->meta_ints = (size_t)4 * R + Hd + 3 * (size_t)R + 64;
+    TRY(dalloc(e, &e->d_meta, e->meta_ints));
+    NDL_CUDA(cudaMallocHost(&e->h_meta, e->meta_ints * sizeof(int32_t)));
+    TRY(dalloc(e, &e->d_ids, (size_t)Hd * 8));
+    TRY(dalloc(e, &e->d_probs, (size_t)Hd * 8));
+    TRY(dalloc(e, &e->d_logp, (size_t)Hd * 8));
+    int words = (c.vocab + 31) / 32;
+    TRY(dalloc(e, &e->d_masks, (size_t)Hd * words));
+    NDL_CUDA(cudaMallocHost(&e->h_out, (size_t)Hd * 8 * 12 + (size_t)Hd * words * 4 + 64));
+    NDL_CUDA(cudaStreamSynchronize(e->stream));
+    return NDL_OK;
+}
+
+void free_slot_pages(ndl_engine *e, int slot, int keep_pages, std::vector<int32_t> *updates) {
+    int32_t *row = e->page_table.data() + (size_t)slot * e->max_pages;
+    for (int i = keep_pages; i < e->max_pages; i++) {
+        if (row[i] >= 0) {
+            e->free_pages.push_back(row[i]);
+            row[i] = -1;
+            if (updates) updates->insert(updates->end(), {slot, i, -1});
+        }
+    }
+}
+
+int check_status(ndl_engine *e) {
+    int st = 0;
+    NDL_CUDA(cudaMemcpyAsync(&st, e->d_status, sizeof(int), cudaMemcpyDeviceToHost, e->stream));
+    NDL_CUDA(cudaStreamSynchronize(e->stream));
+    if (st) {
+        cudaMemsetAsync(e->d_status, 0, sizeof(int), e->stream);
+        if (st & kStatusTimeout) return set_error(NDL_ERR_TIMEOUT, "a kernel wait gave up (status 0x%x)", st);
+        return set_error(NDL_ERR_BOUNDS, "a kernel saw an out-of-range page or token (status 0x%x)", st);
+    }
+    return NDL_OK;
+}
+
+int push_page_updates(ndl_engine *e, const std::vector<int32_t> &updates) {
+    if (updates.empty()) return NDL_OK;
+    // apply on the host mirror's device copy directly: small, synchronous
+    for (size_t i = 0; i < updates.size(); i += 3) {
+        NDL_CUDA(cudaMemcpyAsync(e->d_page_table + (size_t)updates[i] * e->max_pages + updates[i + 1],
+                                 e->page_table.data() + (size_t)updates[i] * e->max_pages + updates[i + 1],
+                                 sizeof(int32_t), cudaMemcpyHostToDevice, e->stream));
+    }
+    NDL_CUDA(cudaStreamSynchronize(e->stream));
+    return NDL_OK;
+}
+
+int check_slot(ndl_engine *e, int slot) {
+    if (!e) return set_error(NDL_ERR_INVALID_ARG, "engine is NULL");
+    if (slot < 0 || slot >= e->ec.slots) return set_error(NDL_ERR_INVALID_ARG, "slot %d out of range", slot);
+    return NDL_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+NDL_API int ndl_engine_create(const ndl_engine_config *ec, const ndl_decoder_config *dc, ndl_engine **out) {
+    NDL_REQUIRE(ec && dc && out, "null argument");
+    *out = nullptr;
+    NDL_REQUIRE(dc->head_dim == kHeadDim, "head_dim must be %d", kHeadDim);
+    NDL_REQUIRE(dc->layers >= 1 && dc->heads >= 1 && dc->dim == dc->heads * dc->head_dim,
+                "dim must equal heads * head_dim");
+    NDL_REQUIRE(dc->ffn >= 32 && dc->ffn % 32 == 0 && dc->dim % 32 == 0, "dim and ffn must be multiples of 32");
+    NDL_REQUIRE(dc->vocab >= 1, "vocab must be positive");
+    NDL_REQUIRE(ec->slots >= 1 && ec->capacity >= kPagePositions && ec->capacity % kPagePositions == 0,
+                "capacity must be a positive multiple of %d", kPagePositions);
+    NDL_REQUIRE(ec->max_rows >= 1 && ec->max_heads >= 1 && ec->max_heads <= ec->max_rows, "bad row limits");
+    int count = 0;
+    if (cudaGetDeviceCount(&count) != cudaSuccess || ec->device < 0 || ec->device >= count) {
+        cudaGetLastError();
+        return set_error(NDL_ERR_NO_DEVICE, "device %d not available", ec->device);
+    }
+    NDL_CUDA(cudaSetDevice(ec->device));
+    ndl_engine *e = new ndl_engine();
+    e->ec = *ec;
+    e->dc = *dc;
+    if (e->dc.rope_theta <= 0.0f) e->dc.rope_theta = 10000.0f;
+    cudaError_t err = cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking);
+    if (err != cudaSuccess) {
+        delete e;
+        return set_error(NDL_ERR_CUDA, "stream: %s", cudaGetErrorString(err));
+    }
+    e->own_stream = true;
+    e->max_pages = ec->capacity / kPagePositions;
+    e->page_bytes = kv_page_bytes(dc->layers, dc->heads);
+    int pages = ec->kv_pages > 0 ? ec->kv_pages : ec->slots * e->max_pages;
+    e->ec.kv_pages = pages;
+    int st = NDL_OK;
+    if (st == NDL_OK) st = dalloc(e, &e->pool, (size_t)pages * e->page_bytes);
+    if (st == NDL_OK) st = dalloc(e, &e->d_page_table, (size_t)ec->slots * e->max_pages);
+    if (st == NDL_OK) st = build_weights(e);
+    if (st == NDL_OK) st = build_buffers(e);
+    if (st != NDL_OK) {
+        ndl_engine_destroy(e);
+        return st;
+    }
+    e->page_table.assign((size_t)ec->slots * e->max_pages, -1);
+    cudaMemcpy(e->d_page_table, e->page_table.data(), e->page_table.size() * 4, cudaMemcpyHostToDevice);
+    e->free_pages.resize(pages);
+    for (int i = 0; i < pages; i++) e->free_pages[i] = pages - 1 - i;  // pop_back yields 0, 1, 2, ...
+    e->slot_len.assign(ec->slots, 0);
+    e->slot_mark.assign(ec->slots, 0);
+    *out = e;
+    return NDL_OK;
+}
+
+NDL_API int ndl_engine_destroy(ndl_engine *e) {
+    if (!e) return NDL_OK;
+    if (e->stream) cudaStreamSynchronize(e->stream);
+    for (void *p : e->allocations) cudaFree(p);
+    if (e->h_meta) cudaFreeHost(e->h_meta);
+    if (e->h_out) cudaFreeHost(e->h_out);
+    if (e->own_stream && e->stream) cudaStreamDestroy(e->stream);
+    delete e;
+    return NDL_OK;
+}
+
+NDL_API int ndl_engine_stream(ndl_engine *e, void **stream) {
+    NDL_REQUIRE(e && stream, "null argument");
+    *stream = e->stream;
+    return NDL_OK;
+}
+
+NDL_API int ndl_engine_tensor(ndl_engine *e, const char *name, int layer, void **ptr, size_t *bytes) {
+    NDL_REQUIRE(e && name && ptr && bytes, "null argument");
+    const ndl_decoder_config &c = e->dc;
+    const size_t d = c.dim, F = c.ffn, V = c.vocab, G = d / 32, GF = F / 32;
+    std::string n(name);
+    if (layer >= 0) {
+        NDL_REQUIRE(layer < c.layers, "layer %d out of range", layer);
+        DeviceLayer &L = e->layers[layer];
+        if (n == "w_qkv") { *ptr = L.w_qkv; *bytes = 3 * d * d; }
+        else if (n == "s_qkv") { *ptr = L.s_qkv; *bytes = 3 * d * G * 2; }
+        else if (n == "w_o") { *ptr = L.w_o; *bytes = d * d; }
+        else if (n == "s_o") { *ptr = L.s_o; *bytes = d * G * 2; }
+        else if (n == "w_gu") { *ptr = L.w_gu; *bytes = 2 * F * d; }
+        else if (n == "s_gu") { *ptr = L.s_gu; *bytes = 2 * F * G * 2; }
+        else if (n == "w_d") { *ptr = L.w_d; *bytes = d * F; }
+        else if (n == "s_d") { *ptr = L.s_d; *bytes = d * GF * 2; }
+        else if (n == "attn_norm") { *ptr = L.attn_norm; *bytes = d * 4; }
+        else if (n == "ffn_norm") { *ptr = L.ffn_norm; *bytes = d * 4; }
+        else return set_error(NDL_ERR_INVALID_ARG, "unknown layer tensor '%s'", name);
+        return NDL_OK;
+    }
+    if (n == "final_norm") { *ptr = e->final_norm; *bytes = d * 4; }
+    else if (n == "embedding") { *ptr = e->embedding; *bytes = V * d * 2; }
+    else if (n == "w_head") { *ptr = e->w_head; *bytes = V * d; }
+    else if (n == "s_head") { *ptr = e->s_head; *bytes = V * G * 2; }
+    else if (n == "rope_cos") { *ptr = e->rope_cos; *bytes = (size_t)e->ec.capacity * (c.head_dim / 2) * 4; }
+    else if (n == "rope_sin") { *ptr = e->rope_sin; *bytes = (size_t)e->ec.capacity * (c.head_dim / 2) * 4; }
+    else if (n == "kv_pool") { *ptr = e->pool; *bytes = (size_t)e->ec.kv_pages * e->page_bytes; }
+    else if (n == "page_table") { *ptr = e->d_page_table; *bytes = e->page_table.size() * 4; }
+    else if (n == "logits") { *ptr = e->logits; *bytes = (size_t)e->ec.max_heads * V * 4; }
+    else return set_error(NDL_ERR_INVALID_ARG, "unknown tensor '%s'", name);
+    return NDL_OK;
+}
+
+NDL_API int ndl_engine_read_tensor(ndl_engine *e, const char *name, int layer, void *host, size_t bytes) {
+    void *ptr = nullptr;
+    size_t have = 0;
+    TRY(ndl_engine_tensor(e, name, layer, &ptr, &have));
+    NDL_REQUIRE(host && bytes <= have, "read of %zu bytes from a %zu-byte tensor", bytes, have);
+    NDL_CUDA(cudaStreamSynchronize(e->stream));
+    NDL_CUDA(cudaMemcpy(host, ptr, bytes, cudaMemcpyDeviceToHost));
+    return NDL_OK;
+}
+
+NDL_API int ndl_engine_page_bytes(ndl_engine *e, size_t *bytes) {
+    NDL_REQUIRE(e && bytes, "null argument");
+    *bytes = e->page_bytes;
+    return NDL_OK;
+}
+
+NDL_API int ndl_slot_length(ndl_engine *e, int slot, int *length) {
+    TRY(check_slot(e, slot));
+    NDL_REQUIRE(length, "length is NULL");
+    *length = e->slot_len[slot];
+    return NDL_OK;
+}
+
+NDL_API int ndl_slot_page(ndl_engine *e, int slot, int index, int *page) {
+    TRY(check_slot(e, slot));
+    NDL_REQUIRE(page && index >= 0 && index < e->max_pages, "bad page index");
+    *page = e->page_table[(size_t)slot * e->max_pages + index];
+    return NDL_OK;
+}
+
+// EngineCore.ResetSlot (src/Needle/Engine.cs:2267-2271): empty the slot.
+NDL_API int ndl_slot_reset(ndl_engine *e, int slot) {
+    TRY(check_slot(e, slot));
+    std::vector<int32_t> updates;
+    free_slot_pages(e, slot, 0, &updates);
+    e->slot_len[slot] = 0;
+    e->slot_mark[slot] = 0;
+    return push_page_updates(e, updates);
+}
+
+// EngineCore.MarkSlot (src/Needle/Engine.cs:2273-2277): remember the length.
+NDL_API int ndl_slot_mark(ndl_engine *e, int slot) {
+    TRY(check_slot(e, slot));
+    e->slot_mark[slot] = e->slot_len[slot];
+    return NDL_OK;
+}
+
+// EngineCore.RewindSlot (src/Needle/Engine.cs:2279-2283): back to the mark;
+// pages wholly past the mark are returned to the pool.
+NDL_API int ndl_slot_rewind(ndl_engine *e, int slot) {
+    TRY(check_slot(e, slot));
+    std::vector<int32_t> updates;
+    int keep = (e->slot_mark[slot] + kPagePositions - 1) / kPagePositions;
+    free_slot_pages(e, slot, keep, &updates);
+    e->slot_len[slot] = e->slot_mark[slot];
+    return push_page_updates(e, updates);
+}
+
+// Fills positions [len, len+count) of a slot with the synthetic prefix K/V
+// (fp16 N(0,1) quantized on load) and advances its length.
+NDL_API int ndl_slot_fill_synthetic(ndl_engine *e, int slot, int count, uint64_t seed, uint64_t session) {
+    TRY(check_slot(e, slot));
+    NDL_REQUIRE(count >= 0, "count < 0");
+    int first = e->slot_len[slot];
+    if (first + count > e->ec.capacity)
+        return set_error(NDL_FAIL_CONTEXT_EXHAUSTED, "slot %d: %d + %d exceeds capacity %d", slot, first, count,
+                         e->ec.capacity);
+    std::vector<int32_t> updates;
+    int32_t *row = e->page_table.data() + (size_t)slot * e->max_pages;
+    for (int p = first / kPagePositions; p * kPagePositions < first + count; p++) {
+        if (row[p] < 0) {
+            if (e->free_pages.empty()) return set_error(NDL_ERR_PAGES_EXHAUSTED, "KV page pool exhausted");
+            row[p] = e->free_pages.back();
+            e->free_pages.pop_back();
+            updates.insert(updates.end(), {slot, p, row[p]});
+        }
+    }
+    TRY(push_page_updates(e, updates));
+    TRY(launch_kv_fill(seed, session, e->dc.layers, e->dc.heads, first, count,
+                       e->d_page_table + (size_t)slot * e->max_pages, e->pool, (long long)e->page_bytes,
+                       e->stream));
+    NDL_CUDA(cudaStreamSynchronize(e->stream));
+    e->slot_len[slot] = first + count;
+    return NDL_OK;
+}
+
+// EngineCore.ForwardBatch (src/Needle/Engine.cs:2303-2350).
+NDL_API int ndl_forward_batch(ndl_engine *e, const int *tokens, const int *row_slots, int rows, const int *head_rows,
+                              int heads) {
+    NDL_REQUIRE(e, "engine is NULL");
+    NDL_REQUIRE(rows >= 1 && rows <= e->ec.max_rows, "rows %d outside 1..%d", rows, e->ec.max_rows);
+    NDL_REQUIRE(heads >= 0 && heads <= e->ec.max_heads && heads <= rows, "heads %d out of range", heads);
+    NDL_REQUIRE(tokens && row_slots && (heads == 0 || head_rows), "null argument");
+    const ndl_decoder_config &c = e->dc;
+    // positions, capacity check, page allocation (host)
+    int32_t *m = e->h_meta;
+    const int R = e->ec.max_rows;
+    e->off_tokens = 0, e->off_slot = R, e->off_pos = 2 * R, e->off_order = 3 * R, e->off_head = 4 * R;
+    e->off_updates = 4 * R + e->ec.max_heads;
+    std::vector<int> advance;
+    advance.reserve(rows);
+    int max_len = 0;
+    for (int r = 0; r < rows; r++) {
+        int slot = row_slots[r];
+        if (slot < 0 || slot >= e->ec.slots) return set_error(NDL_ERR_INVALID_ARG, "row %d: slot %d", r, slot);
+        if (tokens[r] < 0 || tokens[r] >= c.vocab) return set_error(NDL_ERR_INVALID_ARG, "row %d: token %d", r, tokens[r]);
+        int offset = (r > 0 && row_slots[r - 1] == slot) ? (m[e->off_pos + r - 1] - e->slot_len[slot] + 1) : 0;
+        if (r > 0 && row_slots[r - 1] != slot)
+            for (int q = 0; q < r; q++)
+                if (row_slots[q] == slot) return set_error(NDL_ERR_INVALID_ARG, "slot %d rows are not consecutive", slot);
+        int pos = e->slot_len[slot] + offset;
+        if (pos >= e->ec.capacity)
+            return set_error(NDL_FAIL_CONTEXT_EXHAUSTED, "slot %d: context capacity %d exceeded", slot, e->ec.capacity);
+        m[e->off_tokens + r] = tokens[r];
+        m[e->off_slot + r] = slot;
+        m[e->off_pos + r] = pos;
+        max_len = std::max(max_len, pos + 1);
+    }
+    for (int h = 0; h < heads; h++) {
+        if (head_rows[h] < 0 || head_rows[h] >= rows) return set_error(NDL_ERR_INVALID_ARG, "head row %d", head_rows[h]);
+        m[e->off_head + h] = head_rows[h];
+    }
+    // pages for the new positions
+    int n_updates = 0;
+    for (int r = 0; r < rows; r++) {
+        int slot = m[e->off_slot + r], pg = m[e->off_pos + r] / kPagePositions;
+        int32_t &entry = e->page_table[(size_t)slot * e->max_pages + pg];
+        if (entry < 0) {
+            if (e->free_pages.empty()) return set_error(NDL_ERR_PAGES_EXHAUSTED, "KV page pool exhausted");
+            entry = e->free_pages.back();
+            e->free_pages.pop_back();
+            m[e->off_updates + 3 * n_updates] = slot;
+            m[e->off_updates + 3 * n_updates + 1] = pg;
+            m[e->off_updates + 3 * n_updates + 2] = entry;
+            n_updates++;
+        }
+    }
+    // longest rows first (LPT order for the attention work list)
+    std::vector<int> order(rows);
+    for (int r = 0; r < rows; r++) order[r] = r;
+    std::stable_sort(order.begin(), order.end(),
+                     [&](int a, int b) { return m[e->off_pos + a] > m[e->off_pos + b]; });
+    for (int r = 0; r < rows; r++) m[e->off_order + r] = order[r];
+    size_t meta_bytes = (size_t)(e->off_updates + 3 * n_updates) * sizeof(int32_t);
+    cudaStream_t s = e->stream;
+    NDL_CUDA(cudaMemcpyAsync(e->d_meta, m, meta_bytes, cudaMemcpyHostToDevice, s));
+    const int32_t *d_tokens = e->d_meta + e->off_tokens, *d_slot = e->d_meta + e->off_slot;
+    const int32_t *d_pos = e->d_meta + e->off_pos, *d_order = e->d_meta + e->off_order;
+    const int32_t *d_head = e->d_meta + e->off_head;
+    TRY(launch_step_prepare(e->d_meta + e->off_updates, n_updates, e->d_page_table, e->max_pages, d_tokens, rows,
+                            e->embedding, c.vocab, c.dim, e->x, e->d_status, s));
+
+    // attention split: a fixed number of pages per work item, so that a row's
+    // result depends only on its own length (batch-invariant logits)
+    int max_pages_row = 0;
+    for (int r = 0; r < rows; r++) max_pages_row = std::max(max_pages_row, m[e->off_pos + r] / kPagePositions + 1);
+    const int chunk_pages = kAttnChunkPages;
+    const int max_chunks = (max_pages_row + chunk_pages - 1) / chunk_pages;
+
+    const int d = c.dim, F = c.ffn;
+    for (int l = 0; l < c.layers; l++) {
+        const DeviceLayer &L = e->layers[l];
+        TRY(launch_quantize_rows(e->x, L.attn_norm, rows, d, e->qa, e->sa, s));
+        TRY(ndl_matmul_i8g32(e->qa, e->sa, rows, L.w_qkv, L.s_qkv, 3 * d, d, e->qkv, 3 * d, nullptr, nullptr, s));
+        KvWriteArgs kw{e->qkv, 3 * d, d_slot, d_pos, e->d_page_table, e->max_pages, e->pool, (long long)e->page_bytes,
+                       e->ec.kv_pages, e->rope_cos, e->rope_sin, l, c.heads, rows, e->q8, e->qs, e->d_status};
+        TRY(launch_kv_write(kw, s));
+        AttnArgs aa{e->q8, e->qs, d_slot, d_pos, d_order, e->d_page_table, e->max_pages, e->pool,
+                    (long long)e->page_bytes, e->ec.kv_pages, l, c.heads, rows, chunk_pages, max_chunks,
+                    1.0f / sqrtf((float)c.head_dim), e->attn, e->partials, e->arrivals, e->d_status};
+        TRY(launch_attn_decode(aa, s));
+        TRY(launch_quantize_rows(e->attn, nullptr, rows, d, e->qa, e->sa, s));
+        TRY(ndl_matmul_i8g32(e->qa, e->sa, rows, L.w_o, L.s_o, d, d, e->x, d, e->x, nullptr, s));
+        TRY(launch_quantize_rows(e->x, L.ffn_norm, rows, d, e->qa, e->sa, s));
+        TRY(ndl_matmul_i8g32(e->qa, e->sa, rows, L.w_gu, L.s_gu, 2 * F, d, e->gu, 2 * F, nullptr, nullptr, s));
+        TRY(launch_swiglu_quantize(e->gu, rows, F, e->act, e->qa, e->sa, s));
+        TRY(ndl_matmul_i8g32(e->qa, e->sa, rows, L.w_d, L.s_d, d, F, e->x, d, e->x, nullptr, s));
+    }
+    if (heads > 0) {
+        TRY(launch_gather_rows(e->x, d_head, heads, d, e->head_x, s));
+        TRY(launch_quantize_rows(e->head_x, e->final_norm, heads, d, e->qa, e->sa, s));
+        TRY(ndl_matmul_i8g32(e->qa, e->sa, heads, e->w_head, e->s_head, c.vocab, d, e->logits, c.vocab, nullptr,
+                             nullptr, s));
+    }
+    // bookkeeping (src/Needle/Engine.cs:2327-2340): lengths advance per slot run
+    for (int r = 0; r < rows; r++) e->slot_len[m[e->off_slot + r]] = m[e->off_pos + r] + 1;
+    e->last_rows = rows;
+    e->last_heads = heads;
+    return NDL_OK;
+}
+
+NDL_API int ndl_engine_sync(ndl_engine *e) {
+    NDL_REQUIRE(e, "engine is NULL");
+    return check_status(e);
+}
+
+// BatchedEngine.BatchLogitsRow (src/Needle/BatchEngine.cs:37): host copy of
+// the logits of one compact head row of the last forward_batch.
+NDL_API int ndl_batch_logits_row(ndl_engine *e, int compact_row, float *out) {
+    NDL_REQUIRE(e && out, "null argument");
+    NDL_REQUIRE(compact_row >= 0 && compact_row < e->last_heads, "compact row %d out of range", compact_row);
+    NDL_CUDA(cudaMemcpyAsync(out, e->logits + (size_t)compact_row * e->dc.vocab, (size_t)e->dc.vocab * 4,
+                             cudaMemcpyDeviceToHost, e->stream));
+    return check_status(e);
+}
+
+// Greedy / grammar-masked selection over the head rows of the last step:
+// Ops.ArgMaxMasked / ArgMaxMaskedWithProbability (src/Needle/Ops.cs:1223-1330).
+// masks: host [heads][words] (NULL = everything allowed); probs nullable.
+NDL_API int ndl_sample_argmax(ndl_engine *e, const uint32_t *masks, int words, int *ids, float *probs) {
+    NDL_REQUIRE(e && ids, "null argument");
+    const int n = e->last_heads, V = e->dc.vocab;
+    if (n == 0) return NDL_OK;
+    const int max_words = (V + 31) / 32;
+    NDL_REQUIRE(!masks || (words >= 1 && words <= max_words), "words %d outside 1..%d", words, max_words);
+    cudaStream_t s = e->stream;
+    uint8_t *h = static_cast<uint8_t *>(e->h_out);
+    if (masks) {
+        memcpy(h + (size_t)e->ec.max_heads * 96, masks, (size_t)n * words * 4);
+        NDL_CUDA(cudaMemcpyAsync(e->d_masks, h + (size_t)e->ec.max_heads * 96, (size_t)n * words * 4,
+                                 cudaMemcpyHostToDevice, s));
+    }
+    TRY(launch_argmax_masked(e->logits, V, masks ? e->d_masks : nullptr, words, words, V, n, e->d_ids,
+                             probs ? e->d_probs : nullptr, s));
+    NDL_CUDA(cudaMemcpyAsync(h, e->d_ids, (size_t)n * 4, cudaMemcpyDeviceToHost, s));
+    if (probs) NDL_CUDA(cudaMemcpyAsync(h + (size_t)n * 4, e->d_probs, (size_t)n * 4, cudaMemcpyDeviceToHost, s));
+    TRY(check_status(e));
+    memcpy(ids, h, (size_t)n * 4);
+    if (probs) memcpy(probs, h + (size_t)n * 4, (size_t)n * 4);
+    return NDL_OK;
+}
+
+// Beam expansion: Ops.TopKLogSoftmax (src/Needle/Ops.cs:1092-1221) on every
+// head row of the last step.  Outputs [heads][k] on the host.
+NDL_API int ndl_sample_topk(ndl_engine *e, int k, int mask_special_023, int *ids, float *log_probs, float *probs) {
+    NDL_REQUIRE(e && ids && log_probs, "null argument");
+    NDL_REQUIRE(k >= 1 && k <= 8, "k=%d outside 1..8", k);
+    const int n = e->last_heads;
+    if (n == 0) return NDL_OK;
+    cudaStream_t s = e->stream;
+    TRY(launch_topk_logsoftmax(e->logits, e->dc.vocab, e->dc.vocab, k, mask_special_023, n, e->d_ids, e->d_logp,
+                               probs ? e->d_probs : nullptr, s));
+    uint8_t *h = static_cast<uint8_t *>(e->h_out);
+    size_t b = (size_t)n * k * 4;
+    NDL_CUDA(cudaMemcpyAsync(h, e->d_ids, b, cudaMemcpyDeviceToHost, s));
+    NDL_CUDA(cudaMemcpyAsync(h + b, e->d_logp, b, cudaMemcpyDeviceToHost, s));
+    if (probs) NDL_CUDA(cudaMemcpyAsync(h + 2 * b, e->d_probs, b, cudaMemcpyDeviceToHost, s));
+    TRY(check_status(e));
+    memcpy(ids, h, b);
+    memcpy(log_probs, h + b, b);
+    if (probs) memcpy(probs, h + 2 * b, b);
+    return NDL_OK;
+}
+
+}  // extern "C"

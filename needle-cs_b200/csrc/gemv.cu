@@ -4,21 +4,21 @@
 // Replaces Quant.MatMulRows -> Gemv.Rows/Block/Tile4/Tile2
 // (src/Needle/Quant.cs:615-633, src/Needle/Gemv.cs:117-333) for the M < 64
 // decode shapes.  Design:
-//  * A CTA owns 8*R weight rows and one 16-row tile of activations.  Its
-//    warps split the K/32 groups; each group of 8 rows is one
+//  * One warp owns 8 weight rows and one 16-row tile of activations and
+//    walks every 32-column group in ascending order.  Each group is one
 //    mma.sync.m16n8k32 (K = 32 = one group), so the int32 accumulator of an
-//    MMA is exactly D for that group.  Weight bytes are read once, 8 bytes
-//    per lane per group, with L1-bypassing loads.
-//  * D goes to shared memory.  An epilogue pass then sums the groups of
-//    each (t, n) in ascending order with round-to-nearest multiplies and
-//    adds (no FMA), which reproduces the scalar definition bit for bit and
-//    makes a row's result independent of the batch it is in.
-//  * The MMA computes sum_k A[t][k] B[k][n] over a 32-wide k slice.  Any
-//    permutation of k applied to both operands leaves that sum unchanged,
-//    so each lane loads 8 contiguous bytes of its weight row (group bytes
-//    8*tig .. 8*tig+7) and the same 8 bytes of its two activation rows; the
-//    fragment registers are then b0 = bytes 0..3, b1 = bytes 4..7 and
-//    a0/a2 (row gid), a1/a3 (row gid+8) likewise.
+//    MMA is exactly D for that group; the lane then folds its four (t, n)
+//    results into fp32 accumulators with round-to-nearest multiplies and
+//    adds (no FMA), in group order.  That is the scalar definition bit for
+//    bit, and a row's result does not depend on the batch it is in.
+//  * Weight bytes are read once with L1-bypassing 8-byte loads, eight groups
+//    in flight per lane.  The MMA computes sum_k A[t][k] B[k][n] over a
+//    32-wide k slice; any permutation of k applied to both operands leaves
+//    that sum unchanged, so each lane loads 8 contiguous bytes of its weight
+//    row (group bytes 8*tig .. 8*tig+7) and the same 8 bytes of its two
+//    activation rows: b0 = bytes 0..3, b1 = bytes 4..7, a0/a2 (row gid),
+//    a1/a3 (row gid+8) likewise.
+//  * int32 -> fp32 is exact by the 1.5*2^23 trick (|D| <= 32*128*128 < 2^22).
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -39,96 +39,85 @@ __device__ __forceinline__ void mma_s8_16x8x32(int (&d)[4], uint32_t a0, uint32_
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0), "r"(0), "r"(0), "r"(0));
 }
 
-constexpr int kGemvWarps = 4;
+// Exact int32 -> fp32 for |d| < 2^22.
+__device__ __forceinline__ float exact_i2f(int d) { return __int_as_float(d + 0x4B400000) - 12582912.0f; }
 
-template <int R>
+constexpr int kGemvWarps = 4;
+constexpr int kGemvUnroll = 8;  // groups in flight per lane
+
 __global__ void __launch_bounds__(kGemvWarps * 32) gemv_i8g32_kernel(MatmulArgs a) {
-    extern __shared__ int32_t smem_d[];  // [G][16][8R+1]
-    constexpr int NT = 8 * R;            // rows per CTA
-    constexpr int S = NT + 1;            // padded row stride
-    const int G = a.k >> 5;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int gid = lane >> 2, tig = lane & 3;
+    const int tile = blockIdx.x * kGemvWarps + warp;  // 8-row weight tile
+    if (tile * 8 >= a.n) return;
+    const int G = a.k >> 5;
     const int b = blockIdx.z;
     const int8_t *w = a.w + (long long)b * a.w_stride;
     const uint16_t *sw = a.sw + (long long)b * a.sw_stride;
     float *y = a.y + (long long)b * a.y_stride;
-    const int n0 = blockIdx.x * NT;
+
+    const int nl = tile * 8 + gid;  // weight row this lane loads
+    const int nc = tile * 8 + 2 * tig;  // output columns nc, nc+1
     const int t0 = blockIdx.y * 16;
     const int ta = t0 + gid, tb = ta + 8;
     const bool va = ta < a.m, vb = tb < a.m;
+    const bool vl = nl < a.n, vc0 = nc < a.n, vc1 = nc + 1 < a.n;
+    const int8_t *wl = w + (size_t)(vl ? nl : 0) * a.k + 8 * tig;
     const int8_t *qa = a.q + (size_t)(va ? ta : 0) * a.k + 8 * tig;
     const int8_t *qb = a.q + (size_t)(vb ? tb : 0) * a.k + 8 * tig;
-    const int8_t *wrow[R];
-    bool vrow[R];
-#pragma unroll
-    for (int r = 0; r < R; r++) {
-        int n = n0 + 8 * r + gid;
-        vrow[r] = n < a.n;
-        wrow[r] = w + (size_t)(vrow[r] ? n : 0) * a.k + 8 * tig;
-    }
+    const uint16_t *s0p = sw + (size_t)(vc0 ? nc : 0) * G;
+    const uint16_t *s1p = sw + (size_t)(vc1 ? nc + 1 : 0) * G;
+    const float sa_a = va ? a.sa[ta] : 0.0f, sa_b = vb ? a.sa[tb] : 0.0f;
 
-#pragma unroll 2
-    for (int g = warp; g < G; g += kGemvWarps) {
-        uint2 bw[R];
+    float acc0 = 0.0f, acc1 = 0.0f, acc2 = 0.0f, acc3 = 0.0f;
+    for (int g0 = 0; g0 < G; g0 += kGemvUnroll) {
+        uint2 B[kGemvUnroll], A0[kGemvUnroll], A1[kGemvUnroll];
+        uint16_t h0[kGemvUnroll], h1[kGemvUnroll];
 #pragma unroll
-        for (int r = 0; r < R; r++) bw[r] = vrow[r] ? ld_stream_u2(wrow[r] + g * 32) : make_uint2(0u, 0u);
-        uint2 A0 = va ? *reinterpret_cast<const uint2 *>(qa + g * 32) : make_uint2(0u, 0u);
-        uint2 A1 = vb ? *reinterpret_cast<const uint2 *>(qb + g * 32) : make_uint2(0u, 0u);
-        int32_t *dg = smem_d + (size_t)g * 16 * S;
+        for (int u = 0; u < kGemvUnroll; u++) {
+            const int g = g0 + u;
+            const bool in = g < G;
+            B[u] = (in && vl) ? ld_stream_u2(wl + g * 32) : make_uint2(0u, 0u);
+            A0[u] = (in && va) ? __ldg(reinterpret_cast<const uint2 *>(qa + g * 32)) : make_uint2(0u, 0u);
+            A1[u] = (in && vb) ? __ldg(reinterpret_cast<const uint2 *>(qb + g * 32)) : make_uint2(0u, 0u);
+            h0[u] = in ? __ldg(s0p + g) : (uint16_t)0;
+            h1[u] = in ? __ldg(s1p + g) : (uint16_t)0;
+        }
 #pragma unroll
-        for (int r = 0; r < R; r++) {
+        for (int u = 0; u < kGemvUnroll; u++) {
+            if (g0 + u >= G) break;
             int d[4];
-            mma_s8_16x8x32(d, A0.x, A1.x, A0.y, A1.y, bw[r].x, bw[r].y);
-            int col = 8 * r + 2 * tig;
-            dg[gid * S + col] = d[0];
-            dg[gid * S + col + 1] = d[1];
-            dg[(gid + 8) * S + col] = d[2];
-            dg[(gid + 8) * S + col + 1] = d[3];
+            mma_s8_16x8x32(d, A0[u].x, A1[u].x, A0[u].y, A1[u].y, B[u].x, B[u].y);
+            const float s0 = half_to_float_ref_fast(h0[u]), s1 = half_to_float_ref_fast(h1[u]);
+            acc0 = __fadd_rn(acc0, __fmul_rn(__fmul_rn(s0, sa_a), exact_i2f(d[0])));
+            acc1 = __fadd_rn(acc1, __fmul_rn(__fmul_rn(s1, sa_a), exact_i2f(d[1])));
+            acc2 = __fadd_rn(acc2, __fmul_rn(__fmul_rn(s0, sa_b), exact_i2f(d[2])));
+            acc3 = __fadd_rn(acc3, __fmul_rn(__fmul_rn(s1, sa_b), exact_i2f(d[3])));
+            if (a.acc) {
+                const int g = g0 + u;
+                if (va && vc0) a.acc[((size_t)ta * a.n + nc) * G + g] = d[0];
+                if (va && vc1) a.acc[((size_t)ta * a.n + nc + 1) * G + g] = d[1];
+                if (vb && vc0) a.acc[((size_t)tb * a.n + nc) * G + g] = d[2];
+                if (vb && vc1) a.acc[((size_t)tb * a.n + nc + 1) * G + g] = d[3];
+            }
         }
     }
-    __syncthreads();
-
-    for (int p = threadIdx.x; p < 16 * NT; p += kGemvWarps * 32) {
-        int tl = p / NT, nl = p - tl * NT;
-        int t = t0 + tl, n = n0 + nl;
-        if (t >= a.m || n >= a.n) continue;
-        float s_a = a.sa[t];
-        const uint16_t *swr = sw + (size_t)n * G;
-        float accum = 0.0f;
-        for (int g = 0; g < G; g++) {
-            int d = smem_d[((size_t)g * 16 + tl) * S + nl];
-            float scaled = __fmul_rn(half_to_float_ref(swr[g]), s_a);
-            accum = __fadd_rn(accum, __fmul_rn(scaled, __int2float_rn(d)));
-            if (a.acc) a.acc[((size_t)t * a.n + n) * G + g] = d;
-        }
+    auto store = [&](int t, int n, float v) {
         size_t o = (size_t)t * a.ldy + n;
-        y[o] = a.residual ? __fadd_rn(a.residual[o], accum) : accum;
-    }
-}
-
-template <int R>
-static int launch_r(const MatmulArgs &a, cudaStream_t stream) {
-    const int G = a.k >> 5;
-    size_t smem = (size_t)G * 16 * (8 * R + 1) * sizeof(int32_t);
-    if (smem > 48 * 1024) {
-        cudaError_t e = cudaFuncSetAttribute(gemv_i8g32_kernel<R>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)smem);
-        if (e != cudaSuccess) return set_error(NDL_ERR_CUDA, "gemv smem attribute: %s", cudaGetErrorString(e));
-    }
-    dim3 grid((a.n + 8 * R - 1) / (8 * R), (a.m + 15) / 16, a.batch);
-    gemv_i8g32_kernel<R><<<grid, kGemvWarps * 32, smem, stream>>>(a);
-    return check_launch("gemv_i8g32");
+        y[o] = a.residual ? __fadd_rn(a.residual[o], v) : v;
+    };
+    if (va && vc0) store(ta, nc, acc0);
+    if (va && vc1) store(ta, nc + 1, acc1);
+    if (vb && vc0) store(tb, nc, acc2);
+    if (vb && vc1) store(tb, nc + 1, acc3);
 }
 
 int launch_gemv_i8g32(const MatmulArgs &a, cudaStream_t stream) {
-    const int G = a.k >> 5;
-    if (G > 256) return set_error(NDL_ERR_UNSUPPORTED, "gemv: k=%d exceeds 8192", a.k);
-    // Enough CTAs to cover the SMs, and at most ~64 group-rows of D in smem.
-    long long ctas4 = (long long)((a.n + 31) / 32) * ((a.m + 15) / 16) * a.batch;
-    if (G <= 16 && ctas4 >= 2 * 148) return launch_r<4>(a, stream);
-    if (G <= 32 && ctas4 >= 148) return launch_r<2>(a, stream);
-    return launch_r<1>(a, stream);
+    const int tiles = (a.n + 7) / 8;
+    dim3 grid((tiles + kGemvWarps - 1) / kGemvWarps, (a.m + 15) / 16, a.batch);
+    if (grid.y > 65535 || grid.z > 65535) return set_error(NDL_ERR_INVALID_ARG, "gemv grid too large");
+    gemv_i8g32_kernel<<<grid, kGemvWarps * 32, 0, stream>>>(a);
+    return check_launch("gemv_i8g32");
 }
 
 }  // namespace ndl

@@ -24,6 +24,46 @@ struct MatmulArgs {
     int batch;
 };
 
+// RoPE + int8 quantize of q (per head) and k, v (per position and head) into
+// the paged cache.  qkv rows are [q heads | k heads | v heads].
+struct KvWriteArgs {
+    const float *qkv;
+    int ld_qkv;
+    const int32_t *row_slot, *row_pos;
+    const int32_t *page_table;
+    int max_pages;
+    uint8_t *pool;
+    long long page_bytes;
+    int num_pages;
+    const float *rope_cos, *rope_sin;  // [positions][32]
+    int layer, heads, rows;
+    int8_t *q8;  // [rows][heads][64]
+    float *qs;   // [rows][heads]
+    int *status;
+};
+int launch_kv_write(const KvWriteArgs &a, cudaStream_t stream);
+
+constexpr int kPartialFloats = 68;  // 64 outputs + peak + sum, padded to 16 bytes
+
+struct AttnArgs {
+    const int8_t *q;  // [rows][heads][64]
+    const float *qs;  // [rows][heads]
+    const int32_t *row_slot, *row_pos, *row_order;
+    const int32_t *page_table;
+    int max_pages;
+    const uint8_t *pool;
+    long long page_bytes;
+    int num_pages;
+    int layer, heads, rows;
+    int chunk_pages, max_chunks;
+    float inv_sqrt_d;
+    float *out;       // [rows][heads][64]
+    float *partials;  // [rows][heads][max_chunks][kPartialFloats]
+    int *arrivals;    // [rows][heads], zero on entry and on exit
+    int *status;
+};
+int launch_attn_decode(const AttnArgs &a, cudaStream_t stream);
+
 // Streaming int8 GEMV (mma.sync m16n8k32 per 32-column group), any m.
 int launch_gemv_i8g32(const MatmulArgs &a, cudaStream_t stream);
 // tcgen05 kind::i8 GEMM for m >= 64; returns NDL_ERR_UNSUPPORTED when the

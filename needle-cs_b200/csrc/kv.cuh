@@ -1,0 +1,78 @@
+// Paged int8 KV cache layout and the PTX helpers the attention kernels use.
+//
+// A page holds 64 consecutive positions of one slot for every layer.  Inside
+// a page, the block of (layer, head) is one contiguous 8704-byte record
+//     [K int8 64x64][K scale f32 x64][V int8 64x64][V scale f32 x64]
+// so a single 16-byte-aligned bulk copy brings everything attention needs
+// for 64 positions of one head into shared memory.  This replaces the
+// reference's flat per-slot arrays [layer][capacity][kvWidth] + scales
+// (src/Needle/Engine.cs:184-187,220-223) with the same per-(position, head)
+// int8 + fp32-scale contents.
+#pragma once
+
+#include <stdint.h>
+
+namespace ndl {
+
+constexpr int kPagePositions = 64;
+constexpr int kHeadDim = 64;
+constexpr int kKvBlockBytes = 2 * (kPagePositions * kHeadDim + kPagePositions * 4);  // 8704
+constexpr int kKScaleOffset = kPagePositions * kHeadDim;                              // 4096
+constexpr int kVOffset = kKScaleOffset + kPagePositions * 4;                          // 4352
+constexpr int kVScaleOffset = kVOffset + kPagePositions * kHeadDim;                   // 8448
+
+__host__ __device__ __forceinline__ size_t kv_page_bytes(int layers, int heads) {
+    return (size_t)layers * heads * kKvBlockBytes;
+}
+__host__ __device__ __forceinline__ size_t kv_block_offset(int layer, int head, int heads) {
+    return ((size_t)layer * heads + head) * kKvBlockBytes;
+}
+
+// Device status word bits (written by kernels, read by the host).
+constexpr int kStatusTimeout = 1;
+constexpr int kStatusBadPage = 2;
+
+#ifdef __CUDACC__
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+// Non-tensor bulk copy global -> shared, completion counted on `bar`.
+// No multicast: every CTA fetches its own bytes.
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait: gives up after `limit` polls and reports false.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity, uint32_t limit) {
+    for (uint32_t i = 0; i < limit; i++)
+        if (mbar_try_wait(bar, parity)) return true;
+    return false;
+}
+#endif
+
+}  // namespace ndl

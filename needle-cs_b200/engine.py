@@ -1,0 +1,176 @@
+"""Host-side mirror of the reference's BatchedEngine over the C ABI.
+
+Method names and argument meaning follow src/Needle/BatchEngine.cs:5-50
+(Slots, Capacity, VocabSize, SlotLength, ResetSlot, MarkSlot, RewindSlot,
+FeedSlot, ForwardBatch, BatchLogitsRow).  Errors raise NeedleError with the
+ABI status: ContextExhausted (3) where the reference throws
+InvalidOperationException("context capacity exceeded"), invalid argument
+(100) where it throws ArgumentOutOfRangeException.
+"""
+import ctypes
+from dataclasses import dataclass
+
+import numpy as np
+
+from ._native import DecoderConfig, EngineConfig, call, lib
+
+
+@dataclass
+class SyntheticDecoder:
+    """The synthetic Needle-3-shaped decoder of the benchmark configs."""
+    layers: int = 12
+    dim: int = 512
+    heads: int = 8
+    head_dim: int = 64
+    ffn: int = 2048
+    vocab: int = 8192
+    rope_theta: float = 10000.0
+    seed: int = 1
+
+    def native(self):
+        return DecoderConfig(self.layers, self.dim, self.heads, self.head_dim, self.ffn, self.vocab, self.rope_theta,
+                             self.seed)
+
+
+def _i32(a):
+    return np.ascontiguousarray(np.asarray(a, dtype=np.int32))
+
+
+class BatchedEngine:
+    def __init__(self, model=None, slots=8, context_length=1024, chunk_size=64, device=0, max_heads=None,
+                 kv_pages=0):
+        self.model = model or SyntheticDecoder()
+        self.chunk = chunk_size
+        max_heads = max_heads or chunk_size
+        cfg = EngineConfig(device, slots, context_length, kv_pages, chunk_size, max_heads)
+        handle = ctypes.c_void_p()
+        mc = self.model.native()
+        call("ndl_engine_create", ctypes.byref(cfg), ctypes.byref(mc), ctypes.byref(handle))
+        self._h = handle
+        self.slots = slots
+        self.capacity = context_length
+        self.vocab_size = self.model.vocab
+        self.max_heads = max_heads
+        self._last_heads = 0
+
+    # -- lifetime --
+    def close(self):
+        if self._h:
+            lib().ndl_engine_destroy(self._h)
+            self._h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def handle(self):
+        return self._h
+
+    def stream(self):
+        s = ctypes.c_void_p()
+        call("ndl_engine_stream", self._h, ctypes.byref(s))
+        return s.value
+
+    # -- slots (BatchEngine.cs:23-30) --
+    def slot_length(self, slot):
+        n = ctypes.c_int()
+        call("ndl_slot_length", self._h, slot, ctypes.byref(n))
+        return n.value
+
+    def reset_slot(self, slot):
+        call("ndl_slot_reset", self._h, slot)
+
+    def mark_slot(self, slot):
+        call("ndl_slot_mark", self._h, slot)
+
+    def rewind_slot(self, slot):
+        call("ndl_slot_rewind", self._h, slot)
+
+    def slot_page(self, slot, index):
+        p = ctypes.c_int()
+        call("ndl_slot_page", self._h, slot, index, ctypes.byref(p))
+        return p.value
+
+    def fill_synthetic(self, slot, count, seed, session):
+        call("ndl_slot_fill_synthetic", self._h, slot, count, seed, session)
+
+    # -- steps --
+    def forward_batch(self, tokens, row_slots, head_rows=()):
+        """EngineCore.ForwardBatch (Engine.cs:2303-2350)."""
+        t, s, h = _i32(tokens), _i32(row_slots), _i32(head_rows)
+        if t.size != s.size:
+            raise ValueError("one slot per token")
+        call("ndl_forward_batch", self._h, t.ctypes.data, s.ctypes.data, t.size, h.ctypes.data if h.size else None,
+             h.size)
+        self._last_heads = h.size
+
+    def feed_slot(self, slot, tokens, compute_logits=True):
+        """BatchedEngine.FeedSlot / EngineCore.FeedSlot (Engine.cs:2285-2301): chunks of `chunk` rows."""
+        tokens = _i32(tokens)
+        if self.slot_length(slot) + tokens.size > self.capacity:
+            from ._native import NeedleError
+
+            raise NeedleError(3, "context capacity exceeded")
+        for start in range(0, tokens.size, self.chunk):
+            part = tokens[start:start + self.chunk]
+            last = start + part.size == tokens.size
+            heads = [part.size - 1] if (last and compute_logits) else []
+            self.forward_batch(part, [slot] * part.size, heads)
+
+    def batch_logits_row(self, compact_row):
+        out = np.empty(self.vocab_size, np.float32)
+        call("ndl_batch_logits_row", self._h, compact_row, out.ctypes.data)
+        return out
+
+    def sample_argmax(self, masks=None, with_probs=False):
+        n = self._last_heads
+        ids = np.empty(n, np.int32)
+        probs = np.empty(n, np.float32) if with_probs else None
+        if masks is not None:
+            masks = np.ascontiguousarray(masks, dtype=np.uint32).reshape(n, -1)
+            call("ndl_sample_argmax", self._h, masks.ctypes.data, masks.shape[1], ids.ctypes.data,
+                 probs.ctypes.data if with_probs else None)
+        else:
+            call("ndl_sample_argmax", self._h, None, 0, ids.ctypes.data, probs.ctypes.data if with_probs else None)
+        return (ids, probs) if with_probs else ids
+
+    def sample_topk(self, k, mask_special_023=False, with_probs=False):
+        n = self._last_heads
+        ids = np.empty((n, k), np.int32)
+        lp = np.empty((n, k), np.float32)
+        pr = np.empty((n, k), np.float32) if with_probs else None
+        call("ndl_sample_topk", self._h, k, int(mask_special_023), ids.ctypes.data, lp.ctypes.data,
+             pr.ctypes.data if with_probs else None)
+        return ids, lp, pr
+
+    def sync(self):
+        call("ndl_engine_sync", self._h)
+
+    # -- export --
+    def tensor_bytes(self, name, layer=-1):
+        p = ctypes.c_void_p()
+        n = ctypes.c_size_t()
+        call("ndl_engine_tensor", self._h, name.encode(), layer, ctypes.byref(p), ctypes.byref(n))
+        return p.value, n.value
+
+    def read_tensor(self, name, dtype, layer=-1, count=None):
+        _, nbytes = self.tensor_bytes(name, layer)
+        itemsize = np.dtype(dtype).itemsize
+        count = nbytes // itemsize if count is None else count
+        out = np.empty(count, dtype)
+        call("ndl_engine_read_tensor", self._h, name.encode(), layer, out.ctypes.data, count * itemsize)
+        return out
+
+    def page_bytes(self):
+        n = ctypes.c_size_t()
+        call("ndl_engine_page_bytes", self._h, ctypes.byref(n))
+        return n.value

@@ -215,3 +215,58 @@ def rope_tables(theta, qk_dim, positions):
     s = np.empty((positions, half), np.float32)
     lib().ndo_rope_tables(theta, qk_dim, positions, ptr(c), ptr(s))
     return c, s
+
+
+class _Decoder(_c.Structure):
+    _fields_ = [("layers", I), ("dim", I), ("heads", I), ("head_dim", I), ("ffn", I), ("vocab", I),
+                ("rope_theta", F), ("eps", F)] + [
+        (name, _c.POINTER(P)) for name in ("w_qkv", "s_qkv", "w_o", "s_o", "w_gu", "s_gu", "w_d", "s_d",
+                                           "attn_norm", "ffn_norm")] + [
+        ("final_norm", P), ("embedding", P), ("w_head", P), ("s_head", P)]
+
+
+LAYER_TENSORS = {"w_qkv": np.int8, "s_qkv": np.uint16, "w_o": np.int8, "s_o": np.uint16, "w_gu": np.int8,
+                 "s_gu": np.uint16, "w_d": np.int8, "s_d": np.uint16, "attn_norm": np.float32,
+                 "ffn_norm": np.float32}
+
+
+class Decoder:
+    """The synthetic decoder on the CPU (ndo_decoder_row), fed with weights
+    copied from the engine under test."""
+
+    def __init__(self, cfg, layer_weights, final_norm, embedding, w_head, s_head, capacity):
+        self.cfg = cfg
+        self._keep = []
+        L = cfg.layers
+        arrays = {}
+        for name in LAYER_TENSORS:
+            arr = (P * L)()
+            for l in range(L):
+                a = np.ascontiguousarray(layer_weights[l][name])
+                self._keep.append(a)
+                arr[l] = a.ctypes.data
+            arrays[name] = arr
+        self._keep += [arrays]
+        g = [np.ascontiguousarray(x) for x in (final_norm, embedding, w_head, s_head)]
+        self._keep += g
+        self.s = _Decoder(cfg.layers, cfg.dim, cfg.heads, cfg.head_dim, cfg.ffn, cfg.vocab, cfg.rope_theta, 1e-6,
+                          *[_c.cast(arrays[n], _c.POINTER(P)) for n in LAYER_TENSORS],
+                          *[x.ctypes.data for x in g])
+        self.capacity = capacity
+        self.cos, self.sin = rope_tables(cfg.rope_theta, cfg.head_dim, capacity)
+
+    def new_kv(self):
+        c = self.cfg
+        W = c.heads * c.head_dim
+        return {"k": np.zeros((c.layers, self.capacity, W), np.int8),
+                "v": np.zeros((c.layers, self.capacity, W), np.int8),
+                "ks": np.zeros((c.layers, self.capacity, c.heads), np.float32),
+                "vs": np.zeros((c.layers, self.capacity, c.heads), np.float32)}
+
+    def row(self, token, pos, kv):
+        logits = np.empty(self.cfg.vocab, np.float32)
+        st = lib().ndo_decoder_row(_c.byref(self.s), token, pos, self.capacity, ptr(kv["k"]), ptr(kv["v"]),
+                                   ptr(kv["ks"]), ptr(kv["vs"]), ptr(self.cos), ptr(self.sin), ptr(logits))
+        if st != 0:
+            raise MemoryError("oracle scratch allocation failed")
+        return logits

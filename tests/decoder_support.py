@@ -1,0 +1,71 @@
+"""Helpers shared by the decoder parity tests: copy an engine's weights into
+the CPU oracle and regenerate the synthetic prefix K/V on the host."""
+import numpy as np
+
+from conftest import entry
+
+KV_STREAM_SHIFT = 20
+
+
+def oracle_decoder(oracle, engine):
+    cfg = engine.model
+    layers = []
+    for l in range(cfg.layers):
+        layers.append({name: engine.read_tensor(name, dt, layer=l) for name, dt in oracle.LAYER_TENSORS.items()})
+    return oracle.Decoder(cfg, layers, engine.read_tensor("final_norm", np.float32),
+                          engine.read_tensor("embedding", np.uint16), engine.read_tensor("w_head", np.int8),
+                          engine.read_tensor("s_head", np.uint16), engine.capacity)
+
+
+def prefix_kv(ops, oracle, decoder, kv, count, seed, session):
+    """Fill positions [0, count) of an oracle KV dict the way
+    ndl_slot_fill_synthetic does: fp16 normal from (seed, session) at index
+    ((((layer*2 + kind) << 20) + pos) * heads + head) * 64 + d, quantized per
+    (position, head) by the oracle's QuantizeInt8."""
+    cfg = decoder.cfg
+    H = cfg.heads
+    for layer in range(cfg.layers):
+        for kind, (vals, scales) in enumerate((("k", "ks"), ("v", "vs"))):
+            first = ((layer * 2 + kind) << KV_STREAM_SHIFT) * H * 64
+            raw = ops.synth_normal_f16(seed, session, count * H * 64, first=first)
+            x = raw.view(np.float16).astype(np.float32).reshape(count * H, 64)
+            q, s = oracle.quantize_rows(x)
+            kv[vals][layer, :count] = q.reshape(count, H * 64)
+            kv[scales][layer, :count] = s.reshape(count, H)
+
+
+def read_slot_kv(engine, slot, positions):
+    """Reads positions [0, positions) of a slot from the paged pool into the
+    flat reference layout (k, v int8 [layers][positions][H*64]; ks, vs)."""
+    cfg = engine.model
+    H, L = cfg.heads, cfg.layers
+    page_bytes = engine.page_bytes()
+    pool_ptr, pool_bytes = engine.tensor_bytes("kv_pool")
+    n_pages = (positions + 63) // 64
+    pages = [engine.slot_page(slot, i) for i in range(n_pages)]
+    need = (max(pages) + 1) * page_bytes
+    pool = engine.read_tensor("kv_pool", np.uint8, count=need)
+    out = {"k": np.zeros((L, positions, H * 64), np.int8), "v": np.zeros((L, positions, H * 64), np.int8),
+           "ks": np.zeros((L, positions, H), np.float32), "vs": np.zeros((L, positions, H), np.float32)}
+    for p in range(positions):
+        page = pages[p // 64]
+        j = p % 64
+        for l in range(L):
+            for h in range(H):
+                blk = pool[page * page_bytes + (l * H + h) * 8704:][:8704]
+                out["k"][l, p, h * 64:(h + 1) * 64] = blk[j * 64:(j + 1) * 64].view(np.int8)
+                out["ks"][l, p, h] = blk[4096 + 4 * j:4096 + 4 * j + 4].view(np.float32)[0]
+                out["v"][l, p, h * 64:(h + 1) * 64] = blk[4352 + j * 64:4352 + (j + 1) * 64].view(np.int8)
+                out["vs"][l, p, h] = blk[8448 + 4 * j:8448 + 4 * j + 4].view(np.float32)[0]
+    return out
+
+
+def logits_close(got, ref, atol=1e-3, rtol=1e-2):
+    """BASELINE tolerance for logits: max-abs 1e-3 or rel 1e-2 per element."""
+    err = np.abs(got - ref)
+    return bool(np.all((err <= atol) | (err <= rtol * np.abs(ref)))), float(err.max())
+
+
+def top2_margin(x):
+    s = np.sort(x)
+    return float(s[-1] - s[-2])

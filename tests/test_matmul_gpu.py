@@ -72,11 +72,12 @@ def test_matmul_residual_and_ldy(ops, oracle, cuda):
     big = torch.full((m, n + 32), 7.5, device=cuda)
     y = big[:, :n]
     resd = torch.from_numpy(res).to(cuda)
-    # write into a strided view: the ABI takes ldy
+    # write into a strided view: the ABI takes ldy (device tensors kept alive across the call)
     from needle_cs_b200._native import call
 
-    call("ndl_matmul_i8g32", torch.from_numpy(q_ref).to(cuda).data_ptr(), torch.from_numpy(s_ref).to(cuda).data_ptr(),
-         m, torch.from_numpy(w).to(cuda).data_ptr(), torch.from_numpy(sw.view(np.int16)).to(cuda).data_ptr(), n, k,
+    qd, sd = torch.from_numpy(q_ref).to(cuda), torch.from_numpy(s_ref).to(cuda)
+    wd, swd = torch.from_numpy(w).to(cuda), torch.from_numpy(sw.view(np.int16)).to(cuda)
+    call("ndl_matmul_i8g32", qd.data_ptr(), sd.data_ptr(), m, wd.data_ptr(), swd.data_ptr(), n, k,
          y.data_ptr(), n + 32, None, None, torch.cuda.current_stream().cuda_stream)
     torch.cuda.synchronize()
     assert np.array_equal(big[:, :n].cpu().numpy(), y_ref)
