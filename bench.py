@@ -13,7 +13,6 @@ import os
 import statistics
 import subprocess
 import sys
-import threading
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
@@ -43,8 +42,9 @@ class ClockSampler:
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, device_index):
-        self.device_index = device_index
+    def __init__(self, device):
+        # a torch device uuid selects the GPU regardless of CUDA_VISIBLE_DEVICES
+        self.device_index = device if isinstance(device, int) else f"GPU-{device}"
         self.proc = None
         self.lines = []
 
@@ -55,7 +55,7 @@ class ClockSampler:
         try:
             self.file = open(self.path, "w")
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits", "-lms", "100",
+                ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits", "-lms", "50",
                  "-i", str(self.device_index)], stdout=self.file, stderr=subprocess.DEVNULL, text=True)
         except Exception:
             self.proc = None
@@ -205,7 +205,142 @@ class GemvWorkload:
         return calls * self.unit_bytes / dt / 1e9, f"{calls} calls of the M={m} linear, 1 weight set (L2/LLC-warm)"
 
 
-WORKLOADS = {"cfg1": GemvWorkload}
+class DecodeWorkload:
+    """Batched greedy decode of the synthetic 12-layer decoder.
+
+    cfg5 (default): 1024 independent sessions per GPU (global sessions
+    round-robin over ranks), KV lengths U[64,1024], two packed 512-row
+    batches per step.  cfg2: 64 sessions, KV lengths U[16,512], one batch.
+    One step = one decoded token for every session on this GPU: for each
+    batch, ndl_forward_batch + masked/greedy argmax, the ids fed back as the
+    next step's tokens.  value counts the device time of the batches
+    (CUDA events on the engine stream); e2e also counts the host round trip
+    of the token ids between batches."""
+
+    PRESETS = {
+        "cfg5": dict(sessions=1024, batch_rows=512, lo=64, hi=1024, seed=5, name="cfg5_dp_decode"),
+        "cfg2": dict(sessions=64, batch_rows=64, lo=16, hi=512, seed=1, name="cfg2_batched_decode"),
+    }
+
+    def __init__(self, preset="cfg5", steps=20, warmup=3):
+        p = self.PRESETS[preset]
+        self.preset = preset
+        self.name = p["name"]
+        self.sessions, self.batch_rows, self.lo, self.hi, self.seed = (p["sessions"], p["batch_rows"], p["lo"],
+                                                                     p["hi"], p["seed"])
+        self.extra_steps = steps + warmup + 8
+        self.unit_bytes = None
+
+    def model(self):
+        eng_mod = __import__("needle_cs_b200.engine", fromlist=["engine"])
+        return eng_mod, eng_mod.SyntheticDecoder(seed=1)
+
+    def global_layout(self, rank, world):
+        total = self.sessions * world
+        rng = np.random.default_rng(self.seed)
+        lengths = rng.integers(self.lo, self.hi + 1, size=total)
+        tokens = np.random.default_rng(self.seed + 1).integers(0, 8192, size=total).astype(np.int32)
+        gids = np.arange(rank, total, world)[:self.sessions]
+        return gids, lengths[gids].astype(np.int64), tokens[gids]
+
+    def setup(self, device, rank=0, world=1):
+        import torch
+
+        eng_mod, model = self.model()
+        cap = ((self.hi + self.extra_steps + 63) // 64) * 64
+        self.engine = eng_mod.BatchedEngine(model, slots=self.sessions, context_length=cap,
+                                            chunk_size=self.batch_rows, max_heads=self.batch_rows,
+                                            device=device.index or 0)
+        self.gids, self.lengths, self.tokens = self.global_layout(rank, world)
+        for j in range(self.sessions):
+            self.engine.fill_synthetic(j, int(self.lengths[j]), self.seed, int(self.gids[j]))
+        self.stream = torch.cuda.ExternalStream(self.engine.stream())
+        self.batches = [np.arange(b, min(b + self.batch_rows, self.sessions), dtype=np.int32)
+                        for b in range(0, self.sessions, self.batch_rows)]
+        self.attn_bytes = 0
+        self.spans = []
+        self.launches_per_batch = 0
+        torch.cuda.synchronize()
+
+    def step(self, timed=False):
+        import torch
+
+        heads = [np.arange(len(b), dtype=np.int32) for b in self.batches]
+        launches = 0
+        for b, rows in enumerate(self.batches):
+            if timed:
+                ev0 = torch.cuda.Event(enable_timing=True)
+                ev1 = torch.cuda.Event(enable_timing=True)
+                ev0.record(self.stream)
+            self.engine.forward_batch(self.tokens[rows], rows, heads[b])
+            ids = self.engine.sample_argmax()
+            if timed:
+                ev1.record(self.stream)
+                self.spans.append((ev0, ev1))
+                # algorithmic attention bytes: K+V int8 + 2 fp32 scales per position and head,
+                # plus q, q scale and the fp32 output per (row, head)
+                pos = self.lengths[rows] + 1
+                self.attn_bytes += 12 * (int(pos.sum()) * 8 * 136 + len(rows) * 8 * (64 + 4 + 256))
+            self.lengths[rows] += 1
+            self.tokens[rows] = ids
+            launches += 1 + 12 * 10 + 3 + 1
+        return launches
+
+    def units_per_step(self):
+        return self.sessions
+
+    def device_ms(self):
+        return sum(a.elapsed_time(b) for a, b in self.spans)
+
+    def describe(self):
+        return {"workload": self.name, "model": "synthetic needle-3-shaped decoder: 12 layers, d 512, 8x64 heads, "
+                                                "SwiGLU 2048, vocab 8192, int8 weights + fp16 per-32 scales",
+                "sessions_per_gpu": self.sessions, "batch_rows": self.batch_rows, "kv_len": [self.lo, self.hi],
+                "kv_cache": "paged int8, 64 positions per page, fp32 scale per (position, head)",
+                "greedy": True, "l2": "inputs exceed L2 (paged KV of every session is read each step)"}
+
+    # --- CPU restatement on a bounded sample ---
+    def cpu_sample(self, oracle, budget_s=20.0, threads=None):
+        from concurrent.futures import ThreadPoolExecutor
+
+        syn = __import__("needle_cs_b200.synthetic", fromlist=["synthetic"])
+        _, model = self.model()
+        threads = threads or os.cpu_count() or 1
+        gids, lengths, tokens = self.global_layout(0, 1)
+        layers, fnorm, emb, wh, sh = syn.decoder_weights(model)
+        cap = int(lengths.max()) + 2
+        dec = oracle.Decoder(model, layers, fnorm, emb, wh, sh, cap)
+        n = max(1, min(2 * threads, 32))
+        kvs = []
+        for j in range(n):
+            kv = dec.new_kv()
+            for layer in range(model.layers):
+                for kind, (vals, scales) in enumerate((("k", "ks"), ("v", "vs"))):
+                    x = syn.prefix_kv_values(self.seed, int(gids[j]), layer, kind, int(lengths[j]), model.heads)
+                    q, s = oracle.quantize_rows(x.reshape(-1, 64))
+                    kv[vals][layer, :lengths[j]] = q.reshape(int(lengths[j]), -1)
+                    kv[scales][layer, :lengths[j]] = s.reshape(int(lengths[j]), -1)
+            kvs.append(kv)
+
+        def one(j):
+            return dec.row(int(tokens[j]), int(lengths[j]), kvs[j])
+
+        t0 = time.perf_counter()
+        with ThreadPoolExecutor(max_workers=threads) as pool:
+            list(pool.map(one, range(n)))
+        dt = time.perf_counter() - t0
+        return n / dt, threads, (f"{n} sessions x 1 decode token each (KV lengths {int(lengths[:n].min())}.."
+                                 f"{int(lengths[:n].max())}), {threads} threads of the scalar C restatement")
+
+
+WORKLOADS = {"cfg1": GemvWorkload, "cfg2": DecodeWorkload, "cfg5": DecodeWorkload}
+DECODE = ("cfg2", "cfg5")
+
+
+def make_workload(name, args):
+    if name in DECODE:
+        return DecodeWorkload(name, steps=args.steps, warmup=args.warmup)
+    return WORKLOADS[name]()
 
 
 def run_reference(args, rank, world):
@@ -214,21 +349,98 @@ def run_reference(args, rank, world):
         return
     oracle = entry.load_oracle()
     entry.load_package()
-    wl = WORKLOADS[args.workload]()
+    wl = make_workload(args.workload, args)
     wl.ops = __import__("needle_cs_b200.ops", fromlist=["ops"])
     per_step = []
-    for i in range(args.warmup + args.steps):
-        v, sample = wl.cpu_sample(oracle, budget_s=3.0)
-        if i >= args.warmup:
+    if args.workload in DECODE:
+        for i in range(max(1, args.steps // 10)):
+            v, cores, sample = wl.cpu_sample(oracle)
             per_step.append(v)
-    value = statistics.median(per_step)
-    line = {"impl": "reference", "metric": "int8 linear GB/s (algorithmic bytes)", "value": value, "unit": "GB/s",
+        value = statistics.median(per_step)
+        metric, unit = "decode tokens/sec", "tokens/s"
+    else:
+        cores = 1
+        for i in range(args.warmup + args.steps):
+            v, sample = wl.cpu_sample(oracle, budget_s=3.0)
+            if i >= args.warmup:
+                per_step.append(v)
+        value = statistics.median(per_step)
+        metric, unit = "int8 linear GB/s (algorithmic bytes)", "GB/s"
+    line = {"impl": "reference", "metric": metric, "value": value, "unit": unit,
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "int8xint8->int32,f32", "data": "synthetic",
             "config": wl.describe(),
-            "cpu_baseline": {"value": value, "unit": "GB/s", "cores": 1, "kind": "port", "sample": sample},
-            "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            "cpu_baseline": {"value": value, "unit": unit, "cores": cores, "kind": "port", "sample": sample},
+            "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
+
+
+def run_decode(args, rank, world, local):
+    import torch
+
+    entry.load_package().lib()
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    wl = make_workload(args.workload, args)
+    wl.setup(device, rank, world)
+    eng = wl.engine
+    for _ in range(args.warmup):
+        wl.step()
+    eng.sync()
+    eng.profile(True)
+    eng.profile_read(reset=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    launches = 0
+    with ClockSampler(torch.cuda.get_device_properties(device).uuid) as clocks:
+        t_begin = torch.cuda.Event(enable_timing=True)
+        t_end = torch.cuda.Event(enable_timing=True)
+        t_begin.record(wl.stream)
+        for _ in range(args.steps):
+            launches += wl.step(timed=True)
+        t_end.record(wl.stream)
+        torch.cuda.synchronize()
+    eng.sync()
+    prof = eng.profile_read(reset=True)
+    barrier(world)
+    dev_ms = max_over_ranks(wl.device_ms(), world)
+    wall_ms = max_over_ranks(t_begin.elapsed_time(t_end), world)
+    ms_per_step = dev_ms / args.steps
+    value = world * wl.units_per_step() * args.steps / (dev_ms * 1e-3)
+    e2e_value = world * wl.units_per_step() * args.steps / (wall_ms * 1e-3)
+    peak, peak_kind = hbm_peak()
+    total_prof = sum(ms for ms, _ in prof.values()) or 1.0
+    attn_ms, attn_n = prof["attention"]
+    attn_achieved = wl.attn_bytes / (attn_ms * 1e-3) / 1e9 if attn_ms else None
+    kernels = {k: {"ms": round(ms, 3), "launches": n, "share": round(ms / total_prof, 4)} for k, (ms, n) in prof.items()}
+    dominant = max(prof, key=lambda k: prof[k][0])
+    rows_per_batch = wl.batch_rows
+    gemm_flops_per_batch = 2 * rows_per_batch * 12 * (1536 * 512 + 512 * 512 + 4096 * 512 + 512 * 2048) + \
+        2 * rows_per_batch * 8192 * 512
+    gemm_ms = sum(prof[k][0] for k in ("gemm_qkv", "gemm_o", "gemm_gateup", "gemm_down", "head"))
+    n_batches = len(wl.batches) * args.steps
+    line = {"metric": "decode tokens/sec (whole box)", "value": value, "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8xint8->int32,f32", "data": "synthetic",
+            "config": wl.describe(),
+            "roofline": {"bound": "hbm", "kernel": "attn_decode_kernel (paged int8 KV, split-K)",
+                         "achieved": attn_achieved, "peak": peak, "unit": "GB/s",
+                         "frac": attn_achieved / peak if attn_achieved else None, "traffic": None,
+                         "peak_source": peak_kind, "algorithmic_bytes_per_launch": wl.attn_bytes / max(attn_n, 1),
+                         "avg_launch_ms": attn_ms / max(attn_n, 1)},
+            "kernels": kernels, "dominant_kernel_class": dominant,
+            "gemm_int8_tops": gemm_flops_per_batch * n_batches / (gemm_ms * 1e-3) / 1e12 if gemm_ms else None,
+            "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": 3 * wl.sessions * 4,
+                    "d2h_bytes_per_step": wl.sessions * 4, "ms_per_step": wall_ms / args.steps},
+            "gpu_launches": launches,
+            "clocks": clocks.summary()}
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        oracle = entry.load_oracle()
+        v, cores, sample = wl.cpu_sample(oracle)
+        line["cpu_baseline"] = {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    eng.close()
 
 
 def run_ours(args, rank, world, local):
@@ -238,7 +450,7 @@ def run_ours(args, rank, world, local):
     pkg.lib()
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
-    wl = WORKLOADS[args.workload]()
+    wl = make_workload(args.workload, args)
     wl.setup(device)
     stream = torch.cuda.current_stream()
     for _ in range(args.warmup):
@@ -251,7 +463,7 @@ def run_ours(args, rank, world, local):
     barrier(world)
     torch.cuda.synchronize()
     launches = 0
-    with ClockSampler(torch.cuda.current_device()) as clocks:
+    with ClockSampler(torch.cuda.get_device_properties(device).uuid) as clocks:
         t_begin = torch.cuda.Event(enable_timing=True)
         t_end = torch.cuda.Event(enable_timing=True)
         t_begin.record(stream)
@@ -306,13 +518,14 @@ def run_ours(args, rank, world, local):
         print(json.dumps(line), flush=True)
 
 
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="cfg1")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="cfg5")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
@@ -324,7 +537,10 @@ def main():
         return
     rank, world, local = dist_setup(args.gpus)
     try:
-        run_ours(args, rank, world, local)
+        if args.workload in DECODE:
+            run_decode(args, rank, world, local)
+        else:
+            run_ours(args, rank, world, local)
     finally:
         if world > 1:
             import torch.distributed as dist

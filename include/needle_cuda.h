@@ -180,6 +180,28 @@ NDL_API int ndl_engine_page_bytes(ndl_engine *e, size_t *bytes);
  * timeouts) as NDL_ERR_BOUNDS / NDL_ERR_TIMEOUT. */
 NDL_API int ndl_engine_sync(ndl_engine *e);
 
+/* Per-kernel-class device timing (CUDA events on the engine stream), the
+ * B200 counterpart of the reference's IStageClock laps
+ * (src/Needle/StageClock.cs:5-48).  profile_read synchronizes, adds every
+ * recorded interval to ms[class] / launches[class] (arrays of
+ * NDL_PROF_CLASSES, nullable) and optionally resets the totals. */
+enum {
+    NDL_PROF_PREPARE = 0,
+    NDL_PROF_NORM_QUANT,
+    NDL_PROF_GEMM_QKV,
+    NDL_PROF_KV_WRITE,
+    NDL_PROF_ATTENTION,
+    NDL_PROF_GEMM_O,
+    NDL_PROF_GEMM_GATEUP,
+    NDL_PROF_SWIGLU,
+    NDL_PROF_GEMM_DOWN,
+    NDL_PROF_HEAD,
+    NDL_PROF_SAMPLE,
+    NDL_PROF_CLASSES
+};
+NDL_API int ndl_engine_profile(ndl_engine *e, int enable);
+NDL_API int ndl_engine_profile_read(ndl_engine *e, double *ms, long long *launches, int reset);
+
 /* Slot state: BatchedEngine.SlotLength/ResetSlot/MarkSlot/RewindSlot
  * (src/Needle/BatchEngine.cs:23-30 -> src/Needle/Engine.cs:2261-2283). */
 NDL_API int ndl_slot_length(ndl_engine *e, int slot, int *length);

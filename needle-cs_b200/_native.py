@@ -52,7 +52,12 @@ SIGNATURES = {
     "ndl_batch_logits_row": (c_int, [c_void_p, c_int, c_void_p]),
     "ndl_sample_argmax": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p]),
     "ndl_sample_topk": (c_int, [c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p]),
+    "ndl_engine_profile": (c_int, [c_void_p, c_int]),
+    "ndl_engine_profile_read": (c_int, [c_void_p, c_void_p, c_void_p, c_int]),
 }
+
+PROF_CLASSES = ["prepare", "norm_quant", "gemm_qkv", "kv_write", "attention", "gemm_o", "gemm_gateup", "swiglu",
+                "gemm_down", "head", "sample"]
 
 
 class DecoderConfig(ctypes.Structure):

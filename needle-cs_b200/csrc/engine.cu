@@ -90,6 +90,13 @@ struct ndl_engine {
     void *h_out = nullptr;  // pinned sampling results
     int last_rows = 0, last_heads = 0;
     int max_chunks_cap = 0;
+    // per-kernel-class timing (CUDA events on the engine stream)
+    bool profile = false;
+    std::vector<cudaEvent_t> event_pool;
+    size_t events_used = 0;
+    std::vector<std::pair<int, size_t>> pending;  // (class, index of the start event)
+    double prof_ms[NDL_PROF_CLASSES] = {0};
+    long long prof_count[NDL_PROF_CLASSES] = {0};
     // offsets of the last step's metadata in d_meta
     int off_tokens = 0, off_slot = 0, off_pos = 0, off_order = 0, off_head = 0, off_updates = 0;
 };
@@ -296,6 +303,30 @@ int push_page_updates(ndl_engine *e, const std::vector<int32_t> &updates) {
     return NDL_OK;
 }
 
+// Records a start event for `cls`; returns the pending index or -1.
+long prof_begin(ndl_engine *e, int cls) {
+    if (!e->profile) return -1;
+    while (e->event_pool.size() < e->events_used + 2) {
+        cudaEvent_t ev;
+        if (cudaEventCreate(&ev) != cudaSuccess) return -1;
+        e->event_pool.push_back(ev);
+    }
+    size_t i = e->events_used;
+    e->events_used += 2;
+    cudaEventRecord(e->event_pool[i], e->stream);
+    e->pending.push_back({cls, i});
+    return (long)i;
+}
+void prof_end(ndl_engine *e, long i) {
+    if (i >= 0) cudaEventRecord(e->event_pool[i + 1], e->stream);
+}
+struct ProfScope {
+    ndl_engine *e;
+    long i;
+    ProfScope(ndl_engine *e_, int cls) : e(e_), i(prof_begin(e_, cls)) {}
+    ~ProfScope() { prof_end(e, i); }
+};
+
 int check_slot(ndl_engine *e, int slot) {
     if (!e) return set_error(NDL_ERR_INVALID_ARG, "engine is NULL");
     if (slot < 0 || slot >= e->ec.slots) return set_error(NDL_ERR_INVALID_ARG, "slot %d out of range", slot);
@@ -359,6 +390,7 @@ NDL_API int ndl_engine_create(const ndl_engine_config *ec, const ndl_decoder_con
 NDL_API int ndl_engine_destroy(ndl_engine *e) {
     if (!e) return NDL_OK;
     if (e->stream) cudaStreamSynchronize(e->stream);
+    for (cudaEvent_t ev : e->event_pool) cudaEventDestroy(ev);
     for (void *p : e->allocations) cudaFree(p);
     if (e->h_meta) cudaFreeHost(e->h_meta);
     if (e->h_out) cudaFreeHost(e->h_out);
@@ -556,8 +588,11 @@ NDL_API int ndl_forward_batch(ndl_engine *e, const int *tokens, const int *row_s
     const int32_t *d_tokens = e->d_meta + e->off_tokens, *d_slot = e->d_meta + e->off_slot;
     const int32_t *d_pos = e->d_meta + e->off_pos, *d_order = e->d_meta + e->off_order;
     const int32_t *d_head = e->d_meta + e->off_head;
-    TRY(launch_step_prepare(e->d_meta + e->off_updates, n_updates, e->d_page_table, e->max_pages, d_tokens, rows,
-                            e->embedding, c.vocab, c.dim, e->x, e->d_status, s));
+    {
+        ProfScope p(e, NDL_PROF_PREPARE);
+        TRY(launch_step_prepare(e->d_meta + e->off_updates, n_updates, e->d_page_table, e->max_pages, d_tokens, rows,
+                                e->embedding, c.vocab, c.dim, e->x, e->d_status, s));
+    }
 
     // attention split: a fixed number of pages per work item, so that a row's
     // result depends only on its own length (batch-invariant logits)
@@ -569,23 +604,55 @@ NDL_API int ndl_forward_batch(ndl_engine *e, const int *tokens, const int *row_s
     const int d = c.dim, F = c.ffn;
     for (int l = 0; l < c.layers; l++) {
         const DeviceLayer &L = e->layers[l];
-        TRY(launch_quantize_rows(e->x, L.attn_norm, rows, d, e->qa, e->sa, s));
-        TRY(ndl_matmul_i8g32(e->qa, e->sa, rows, L.w_qkv, L.s_qkv, 3 * d, d, e->qkv, 3 * d, nullptr, nullptr, s));
-        KvWriteArgs kw{e->qkv, 3 * d, d_slot, d_pos, e->d_page_table, e->max_pages, e->pool, (long long)e->page_bytes,
-                       e->ec.kv_pages, e->rope_cos, e->rope_sin, l, c.heads, rows, e->q8, e->qs, e->d_status};
-        TRY(launch_kv_write(kw, s));
-        AttnArgs aa{e->q8, e->qs, d_slot, d_pos, d_order, e->d_page_table, e->max_pages, e->pool,
-                    (long long)e->page_bytes, e->ec.kv_pages, l, c.heads, rows, chunk_pages, max_chunks,
-                    1.0f / sqrtf((float)c.head_dim), e->attn, e->partials, e->arrivals, e->d_status};
-        TRY(launch_attn_decode(aa, s));
-        TRY(launch_quantize_rows(e->attn, nullptr, rows, d, e->qa, e->sa, s));
-        TRY(ndl_matmul_i8g32(e->qa, e->sa, rows, L.w_o, L.s_o, d, d, e->x, d, e->x, nullptr, s));
-        TRY(launch_quantize_rows(e->x, L.ffn_norm, rows, d, e->qa, e->sa, s));
-        TRY(ndl_matmul_i8g32(e->qa, e->sa, rows, L.w_gu, L.s_gu, 2 * F, d, e->gu, 2 * F, nullptr, nullptr, s));
-        TRY(launch_swiglu_quantize(e->gu, rows, F, e->act, e->qa, e->sa, s));
-        TRY(ndl_matmul_i8g32(e->qa, e->sa, rows, L.w_d, L.s_d, d, F, e->x, d, e->x, nullptr, s));
+        {
+            ProfScope p(e, NDL_PROF_NORM_QUANT);
+            TRY(launch_quantize_rows(e->x, L.attn_norm, rows, d, e->qa, e->sa, s));
+        }
+        {
+            ProfScope p(e, NDL_PROF_GEMM_QKV);
+            TRY(ndl_matmul_i8g32(e->qa, e->sa, rows, L.w_qkv, L.s_qkv, 3 * d, d, e->qkv, 3 * d, nullptr, nullptr, s));
+        }
+        {
+            ProfScope p(e, NDL_PROF_KV_WRITE);
+            KvWriteArgs kw{e->qkv, 3 * d, d_slot, d_pos, e->d_page_table, e->max_pages, e->pool,
+                           (long long)e->page_bytes, e->ec.kv_pages, e->rope_cos, e->rope_sin, l, c.heads, rows,
+                           e->q8, e->qs, e->d_status};
+            TRY(launch_kv_write(kw, s));
+        }
+        {
+            ProfScope p(e, NDL_PROF_ATTENTION);
+            AttnArgs aa{e->q8, e->qs, d_slot, d_pos, d_order, e->d_page_table, e->max_pages, e->pool,
+                        (long long)e->page_bytes, e->ec.kv_pages, l, c.heads, rows, chunk_pages, max_chunks,
+                        1.0f / sqrtf((float)c.head_dim), e->attn, e->partials, e->arrivals, e->d_status};
+            TRY(launch_attn_decode(aa, s));
+        }
+        {
+            ProfScope p(e, NDL_PROF_NORM_QUANT);
+            TRY(launch_quantize_rows(e->attn, nullptr, rows, d, e->qa, e->sa, s));
+        }
+        {
+            ProfScope p(e, NDL_PROF_GEMM_O);
+            TRY(ndl_matmul_i8g32(e->qa, e->sa, rows, L.w_o, L.s_o, d, d, e->x, d, e->x, nullptr, s));
+        }
+        {
+            ProfScope p(e, NDL_PROF_NORM_QUANT);
+            TRY(launch_quantize_rows(e->x, L.ffn_norm, rows, d, e->qa, e->sa, s));
+        }
+        {
+            ProfScope p(e, NDL_PROF_GEMM_GATEUP);
+            TRY(ndl_matmul_i8g32(e->qa, e->sa, rows, L.w_gu, L.s_gu, 2 * F, d, e->gu, 2 * F, nullptr, nullptr, s));
+        }
+        {
+            ProfScope p(e, NDL_PROF_SWIGLU);
+            TRY(launch_swiglu_quantize(e->gu, rows, F, e->act, e->qa, e->sa, s));
+        }
+        {
+            ProfScope p(e, NDL_PROF_GEMM_DOWN);
+            TRY(ndl_matmul_i8g32(e->qa, e->sa, rows, L.w_d, L.s_d, d, F, e->x, d, e->x, nullptr, s));
+        }
     }
     if (heads > 0) {
+        ProfScope p(e, NDL_PROF_HEAD);
         TRY(launch_gather_rows(e->x, d_head, heads, d, e->head_x, s));
         TRY(launch_quantize_rows(e->head_x, e->final_norm, heads, d, e->qa, e->sa, s));
         TRY(ndl_matmul_i8g32(e->qa, e->sa, heads, e->w_head, e->s_head, c.vocab, d, e->logits, c.vocab, nullptr,
@@ -595,6 +662,31 @@ NDL_API int ndl_forward_batch(ndl_engine *e, const int *tokens, const int *row_s
     for (int r = 0; r < rows; r++) e->slot_len[m[e->off_slot + r]] = m[e->off_pos + r] + 1;
     e->last_rows = rows;
     e->last_heads = heads;
+    return NDL_OK;
+}
+
+NDL_API int ndl_engine_profile(ndl_engine *e, int enable) {
+    NDL_REQUIRE(e, "engine is NULL");
+    e->profile = enable != 0;
+    return NDL_OK;
+}
+
+NDL_API int ndl_engine_profile_read(ndl_engine *e, double *ms, long long *launches, int reset) {
+    NDL_REQUIRE(e, "engine is NULL");
+    NDL_CUDA(cudaStreamSynchronize(e->stream));
+    for (auto &pr : e->pending) {
+        float t = 0.0f;
+        NDL_CUDA(cudaEventElapsedTime(&t, e->event_pool[pr.second], e->event_pool[pr.second + 1]));
+        e->prof_ms[pr.first] += t;
+        e->prof_count[pr.first] += 1;
+    }
+    e->pending.clear();
+    e->events_used = 0;
+    for (int i = 0; i < NDL_PROF_CLASSES; i++) {
+        if (ms) ms[i] = e->prof_ms[i];
+        if (launches) launches[i] = e->prof_count[i];
+        if (reset) e->prof_ms[i] = 0.0, e->prof_count[i] = 0;
+    }
     return NDL_OK;
 }
 
@@ -629,8 +721,11 @@ NDL_API int ndl_sample_argmax(ndl_engine *e, const uint32_t *masks, int words, i
         NDL_CUDA(cudaMemcpyAsync(e->d_masks, h + (size_t)e->ec.max_heads * 96, (size_t)n * words * 4,
                                  cudaMemcpyHostToDevice, s));
     }
-    TRY(launch_argmax_masked(e->logits, V, masks ? e->d_masks : nullptr, words, words, V, n, e->d_ids,
-                             probs ? e->d_probs : nullptr, s));
+    {
+        ProfScope p(e, NDL_PROF_SAMPLE);
+        TRY(launch_argmax_masked(e->logits, V, masks ? e->d_masks : nullptr, words, words, V, n, e->d_ids,
+                                 probs ? e->d_probs : nullptr, s));
+    }
     NDL_CUDA(cudaMemcpyAsync(h, e->d_ids, (size_t)n * 4, cudaMemcpyDeviceToHost, s));
     if (probs) NDL_CUDA(cudaMemcpyAsync(h + (size_t)n * 4, e->d_probs, (size_t)n * 4, cudaMemcpyDeviceToHost, s));
     TRY(check_status(e));
@@ -647,8 +742,11 @@ NDL_API int ndl_sample_topk(ndl_engine *e, int k, int mask_special_023, int *ids
     const int n = e->last_heads;
     if (n == 0) return NDL_OK;
     cudaStream_t s = e->stream;
-    TRY(launch_topk_logsoftmax(e->logits, e->dc.vocab, e->dc.vocab, k, mask_special_023, n, e->d_ids, e->d_logp,
-                               probs ? e->d_probs : nullptr, s));
+    {
+        ProfScope p(e, NDL_PROF_SAMPLE);
+        TRY(launch_topk_logsoftmax(e->logits, e->dc.vocab, e->dc.vocab, k, mask_special_023, n, e->d_ids, e->d_logp,
+                                   probs ? e->d_probs : nullptr, s));
+    }
     uint8_t *h = static_cast<uint8_t *>(e->h_out);
     size_t b = (size_t)n * k * 4;
     NDL_CUDA(cudaMemcpyAsync(h, e->d_ids, b, cudaMemcpyDeviceToHost, s));

@@ -12,7 +12,7 @@ from dataclasses import dataclass
 
 import numpy as np
 
-from ._native import DecoderConfig, EngineConfig, call, lib
+from ._native import PROF_CLASSES, DecoderConfig, EngineConfig, call, lib
 
 
 @dataclass
@@ -151,6 +151,16 @@ class BatchedEngine:
         call("ndl_sample_topk", self._h, k, int(mask_special_023), ids.ctypes.data, lp.ctypes.data,
              pr.ctypes.data if with_probs else None)
         return ids, lp, pr
+
+    def profile(self, enable=True):
+        call("ndl_engine_profile", self._h, int(enable))
+
+    def profile_read(self, reset=True):
+        """{class: (ms, launches)} accumulated since the last reset."""
+        ms = np.zeros(len(PROF_CLASSES), np.float64)
+        n = np.zeros(len(PROF_CLASSES), np.int64)
+        call("ndl_engine_profile_read", self._h, ms.ctypes.data, n.ctypes.data, int(reset))
+        return {c: (float(ms[i]), int(n[i])) for i, c in enumerate(PROF_CLASSES)}
 
     def sync(self):
         call("ndl_engine_sync", self._h)

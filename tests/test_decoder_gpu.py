@@ -162,3 +162,19 @@ def test_topk_logsoftmax(small, oracle):
         assert list(ids[r]) == list(ri)
         assert np.allclose(lp[r], rl, atol=1e-5)
         assert np.allclose(pr[r], rp, rtol=1e-5)
+
+
+def test_host_generation_matches_device(small):
+    """needle_cs_b200.synthetic rebuilds the engine's device weights bit for bit."""
+    import importlib
+
+    syn = importlib.import_module("needle_cs_b200.synthetic")
+    layers, fnorm, emb, wh, sh = syn.decoder_weights(small.model)
+    for l, t in enumerate(layers):
+        for name, arr in t.items():
+            got = small.read_tensor(name, arr.dtype, layer=l)
+            assert np.array_equal(got, arr), (l, name)
+    assert np.array_equal(small.read_tensor("final_norm", np.float32), fnorm)
+    assert np.array_equal(small.read_tensor("embedding", np.uint16), emb)
+    assert np.array_equal(small.read_tensor("w_head", np.int8), wh)
+    assert np.array_equal(small.read_tensor("s_head", np.uint16), sh)
