@@ -7,11 +7,12 @@
 //
 // Decode attention (Scalar.AttentionHead src/Needle/Scalar.cs:290-312,
 // AttentionBatch.ExecuteChunk + MergePartials src/Needle/Blocks.cs:750-990):
-// one warp per (row, head, chunk of pages).  Each page's 8704-byte (layer,
-// head) record arrives in shared memory by one cp.async.bulk (3-stage ring,
-// mbarrier completion, bounded waits).  Scores are exact int8 dots scaled by
-// ks * (qs / sqrt(d)); softmax is online (running max, rescaled sum) in fp32
-// with expf; V is accumulated in fp32.  A row split into several chunks
+// persistent warps stream (row, head, chunk of pages) items.  Each page's
+// 8704-byte (layer, head) record arrives in shared memory by one
+// cp.async.bulk (3-stage ring, mbarrier completion, bounded waits).  Scores
+// are exact int8 dots (mma.sync s8) scaled by ks * (qs / sqrt(d)); softmax
+// is online (running max, rescaled sum) in fp32 with expf; V is accumulated
+// in fp32 by mma.sync f16 with hi/lo-split probability weights.  A row split into several chunks
 // writes (peak, sum, unnormalised output) partials and the last chunk to
 // finish merges them with exp(peak - max) weights, like MergePartials.
 #include "common.cuh"
@@ -67,8 +68,8 @@ __global__ void __launch_bounds__(256) kv_write_kernel(KvWriteArgs a) {
         float hi = __fadd_rn(__fmul_rn(x1, c), __fmul_rn(x0, s));
         float scale = warp_quantize64(lo, hi, lo8, hi8);
         int8_t *qo = a.q8 + ((size_t)row * a.heads + head) * kHeadDim;
-        qo[lane] = lo8;
-        qo[lane + 32] = hi8;
+        qo[k_slot(lane)] = lo8;
+        qo[k_slot(lane + 32)] = hi8;
         if (lane == 0) a.qs[(size_t)row * a.heads + head] = scale;
     }
     const int pg = pos / kPagePositions, j = pos - pg * kPagePositions;
@@ -84,8 +85,8 @@ __global__ void __launch_bounds__(256) kv_write_kernel(KvWriteArgs a) {
         float hi = __fadd_rn(__fmul_rn(x1, c), __fmul_rn(x0, s));
         float scale = warp_quantize64(lo, hi, lo8, hi8);
         if (ok) {
-            blk[j * kHeadDim + lane] = (uint8_t)lo8;
-            blk[j * kHeadDim + lane + 32] = (uint8_t)hi8;
+            blk[j * kHeadDim + k_slot(lane)] = (uint8_t)lo8;
+            blk[j * kHeadDim + k_slot(lane + 32)] = (uint8_t)hi8;
             if (lane == 0) reinterpret_cast<float *>(blk + kKScaleOffset)[j] = scale;
         }
     }
@@ -94,8 +95,8 @@ __global__ void __launch_bounds__(256) kv_write_kernel(KvWriteArgs a) {
         const float *vb = base + 2 * width;
         float scale = warp_quantize64(vb[lane], vb[lane + 32], lo8, hi8);
         if (ok) {
-            blk[kVOffset + j * kHeadDim + lane] = (uint8_t)lo8;
-            blk[kVOffset + j * kHeadDim + lane + 32] = (uint8_t)hi8;
+            blk[kVOffset + lane * kHeadDim + v_slot(j)] = (uint8_t)(lo8 + 128);
+            blk[kVOffset + (lane + 32) * kHeadDim + v_slot(j)] = (uint8_t)(hi8 + 128);
             if (lane == 0) reinterpret_cast<float *>(blk + kVScaleOffset)[j] = scale;
         }
     }
@@ -111,7 +112,7 @@ int launch_kv_write(const KvWriteArgs &a, cudaStream_t stream) {
 // ------------------------------------------------------ decode attention --
 constexpr int kAttnWarps = 4;
 constexpr int kAttnStages = 3;
-constexpr int kWarpSmem = kAttnStages * kKvBlockBytes + 64 + 64;  // ring + barriers + query
+constexpr int kWarpSmem = kAttnStages * kKvBlockBytes + 64;  // ring + barriers
 constexpr uint32_t kWaitLimit = 1u << 22;
 
 // int8x4 -> 4 floats exactly: bias each byte by 128, splice it under the
@@ -124,23 +125,71 @@ __device__ __forceinline__ void i8x4_to_f32(uint32_t v, float (&f)[4]) {
     f[3] = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7543)) - 8388736.0f;
 }
 
+// Work item i = (row in LPT order, head, chunk) with chunk innermost.
+struct AttnItem {
+    int row, head, chunk, n_chunks, first_page, n_pages, len, slot;
+};
+
+__device__ __forceinline__ bool attn_item(const AttnArgs &a, int i, AttnItem &it) {
+    const int chunk = i % a.max_chunks;
+    const int rh = i / a.max_chunks;
+    it.head = rh % a.heads;
+    const int ri = rh / a.heads;
+    it.row = a.row_order ? a.row_order[ri] : ri;
+    it.len = a.row_pos[it.row] + 1;
+    const int pages = (it.len + kPagePositions - 1) / kPagePositions;
+    it.n_chunks = (pages + a.chunk_pages - 1) / a.chunk_pages;
+    if (chunk >= it.n_chunks) return false;
+    it.chunk = chunk;
+    it.first_page = chunk * a.chunk_pages;
+    it.n_pages = min(pages, it.first_page + a.chunk_pages) - it.first_page;
+    it.slot = a.row_slot[it.row];
+    return true;
+}
+
+__device__ __forceinline__ void mma_s8_m16n8k32(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                                uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};\n"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void mma_f16_m16n8k16(float (&d)[4], uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};\n"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
+}
+// Two biased bytes (v + 128) -> exact fp16 pair: splice under the exponent of
+// 1024 and subtract 1152.
+__device__ __forceinline__ uint32_t u8x2_to_h2(uint32_t word, uint32_t selector) {
+    uint32_t h = __byte_perm(word, 0x64646464u, selector);
+    __half2 r = __hsub2(*reinterpret_cast<__half2 *>(&h), __floats2half2_rn(1152.0f, 1152.0f));
+    return *reinterpret_cast<uint32_t *>(&r);
+}
+__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
+    __half2 r = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t *>(&r);
+}
+
+// Persistent: each warp walks items warp_gid, warp_gid + W, ... and streams
+// their pages through its 3-stage ring without draining between items.
+// Per page (64 positions):
+//  * QK: mma.sync m16n8k32 s8, A = the query in every row, B = K (k = dims,
+//    n = positions): exact int32 dots; lane L ends up owning positions 2L and
+//    2L+1 for the softmax.
+//  * PV: mma.sync m16n8k16 f16 -> f32, A row 0 = fp16(w'), row 1 =
+//    fp16(w' - row 0) with w' = p * vs * 2^e (hi/lo split, ~22-bit
+//    weights), B = V (exact in fp16).  e keeps w' below 2^12 and is folded
+//    into the online-softmax rescale.
 __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(AttnArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const long long item = (long long)blockIdx.x * kAttnWarps + warp;
-    const int chunk = (int)(item % a.max_chunks);
-    const long long rh = item / a.max_chunks;
-    const int head = (int)(rh % a.heads);
-    const int ri = (int)(rh / a.heads);
-    if (ri >= a.rows) return;
-    const int row = a.row_order ? a.row_order[ri] : ri;
-    const int len = a.row_pos[row] + 1;
-    const int n_pages = (len + kPagePositions - 1) / kPagePositions;
-    const int n_chunks = (n_pages + a.chunk_pages - 1) / a.chunk_pages;
-    if (chunk >= n_chunks) return;
-    const int first_page = chunk * a.chunk_pages;
-    const int n_it = min(n_pages, first_page + a.chunk_pages) - first_page;
-    const int slot = a.row_slot[row];
+    const int gid = lane >> 2, tig = lane & 3;
+    const int W = gridDim.x * kAttnWarps;
+    const int n_items = a.rows * a.heads * a.max_chunks;
 
     uint8_t *ring = smem + warp * kWarpSmem;
     uint64_t *bars = reinterpret_cast<uint64_t *>(ring + kAttnStages * kKvBlockBytes);
@@ -150,150 +199,203 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(AttnArgs a
     }
     __syncwarp();
 
-    auto issue = [&](int it) {  // lane 0 only
-        const int pg = first_page + it;
-        const int page = a.page_table[(size_t)slot * a.max_pages + pg];
-        uint64_t *bar = &bars[it % kAttnStages];
+    // producer cursor (lane 0): next page to issue
+    int p_item = blockIdx.x * kAttnWarps + warp - W;
+    AttnItem pit{};
+    int p_page = 0, p_left = 0;
+    unsigned issued = 0;
+    auto advance_producer = [&]() -> bool {
+        while (p_left == 0) {
+            p_item += W;
+            if (p_item >= n_items) return false;
+            if (attn_item(a, p_item, pit)) {
+                p_page = pit.first_page;
+                p_left = pit.n_pages;
+            }
+        }
+        return true;
+    };
+    auto issue_one = [&]() {  // lane 0 only; requires p_left > 0
+        uint64_t *bar = &bars[issued % kAttnStages];
+        const int page = a.page_table[(size_t)pit.slot * a.max_pages + p_page];
         if (page < 0 || page >= a.num_pages) {
             if (a.status) atomicOr(a.status, kStatusBadPage);
             asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-            return;
+        } else {
+            const uint8_t *src = a.pool + (size_t)page * a.page_bytes + kv_block_offset(a.layer, pit.head, a.heads);
+            fence_proxy_async_smem();
+            mbar_arrive_expect_tx(bar, kKvBlockBytes);
+            bulk_g2s(ring + (issued % kAttnStages) * kKvBlockBytes, src, kKvBlockBytes, bar);
         }
-        const uint8_t *src = a.pool + (size_t)page * a.page_bytes + kv_block_offset(a.layer, head, a.heads);
-        fence_proxy_async_smem();
-        mbar_arrive_expect_tx(bar, kKvBlockBytes);
-        bulk_g2s(ring + (it % kAttnStages) * kKvBlockBytes, src, kKvBlockBytes, bar);
+        issued++;
+        p_page++;
+        p_left--;
     };
     if (lane == 0)
-        for (int it = 0; it < min(kAttnStages, n_it); it++) issue(it);
+        for (int k = 0; k < kAttnStages && advance_producer(); k++) issue_one();
 
-    // the query row, staged in shared memory (lanes read rotated 16-byte chunks)
-    uint4 *qsm = reinterpret_cast<uint4 *>(ring + kAttnStages * kKvBlockBytes + 64);
-    if (lane < 4) qsm[lane] = reinterpret_cast<const uint4 *>(a.q + ((size_t)row * a.heads + head) * kHeadDim)[lane];
-    __syncwarp();
-    const float scale = __fmul_rn(a.qs[(size_t)row * a.heads + head], a.inv_sqrt_d);
-
-    float m = -INFINITY, l = 0.0f;
-    float o[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-    const int par = lane >> 4;          // PV: even (0) or odd (1) positions
-    const int dd = 4 * (lane & 15);     // PV: this lane's 4 dims
-    int it = 0;
+    unsigned consumed = 0;
     bool timed_out = false;
-    for (; it < n_it; it++) {
-        const int stage = it % kAttnStages;
-        if (!mbar_wait_bounded(&bars[stage], (it / kAttnStages) & 1, kWaitLimit)) {
-            timed_out = true;
-            break;
-        }
-        const uint8_t *blk = ring + stage * kKvBlockBytes;
-        const int valid = min(kPagePositions, len - (first_page + it) * kPagePositions);
-        // scores for positions lane and lane + 32 (16-byte chunks rotated per lane pair: no bank conflicts)
-        float sc[2];
+    for (int item = blockIdx.x * kAttnWarps + warp; item < n_items && !timed_out; item += W) {
+        AttnItem it;
+        if (!attn_item(a, item, it)) continue;
+        // query (K dim order): chunk tig = words for both k-steps
+        const uint4 qv = __ldg(reinterpret_cast<const uint4 *>(a.q + ((size_t)it.row * a.heads + it.head) * kHeadDim) +
+                               tig);
+        const float scale = __fmul_rn(a.qs[(size_t)it.row * a.heads + it.head], a.inv_sqrt_d);
+        float m = -INFINITY, l = 0.0f;
+        int e_acc = 12;  // power-of-two scale currently applied to the accumulators
+        float acc[8][4];
 #pragma unroll
-        for (int h = 0; h < 2; h++) {
-            const int j = lane + 32 * h;
-            const uint4 *krow = reinterpret_cast<const uint4 *>(blk + j * kHeadDim);
-            int dot = 0;
-#pragma unroll
-            for (int c = 0; c < 4; c++) {
-                const int cc = (c + (lane >> 1)) & 3;
-                const uint4 kv = krow[cc];
-                const uint4 qv = qsm[cc];
-                dot = __dp4a((int)kv.x, (int)qv.x, dot);
-                dot = __dp4a((int)kv.y, (int)qv.y, dot);
-                dot = __dp4a((int)kv.z, (int)qv.z, dot);
-                dot = __dp4a((int)kv.w, (int)qv.w, dot);
+        for (int nt = 0; nt < 8; nt++) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.0f;
+        for (int pg = 0; pg < it.n_pages; pg++) {
+            const int stage = consumed % kAttnStages;
+            if (!mbar_wait_bounded(&bars[stage], (consumed / kAttnStages) & 1, kWaitLimit)) {
+                timed_out = true;
+                break;
             }
-            const float ks = reinterpret_cast<const float *>(blk + kKScaleOffset)[j];
-            sc[h] = j < valid ? __fmul_rn(__fmul_rn(__int2float_rn(dot), ks), scale) : -INFINITY;
-        }
-        const float m_new = fmaxf(m, warp_max_f(fmaxf(sc[0], sc[1])));
-        const float corr = expf(m - m_new);
-        const float p0 = lane < valid ? expf(sc[0] - m_new) : 0.0f;
-        const float p1 = lane + 32 < valid ? expf(sc[1] - m_new) : 0.0f;
-        l = l * corr + warp_sum_f(p0 + p1);
-        m = m_new;
-        const float *vsc = reinterpret_cast<const float *>(blk + kVScaleOffset);
-        const float w0 = lane < valid ? p0 * vsc[lane] : 0.0f;
-        const float w1 = lane + 32 < valid ? p1 * vsc[lane + 32] : 0.0f;
+            const uint8_t *blk = ring + stage * kKvBlockBytes;
+            const int valid = min(kPagePositions, it.len - (it.first_page + pg) * kPagePositions);
+            // ---- QK: dots for positions nt*8 + 2*tig + {0,1}, every n-tile ----
+            int dot0 = 0, dot1 = 0;
 #pragma unroll
-        for (int i = 0; i < 4; i++) o[i] *= corr;
-        const uint8_t *vbase = blk + kVOffset + dd;
-#pragma unroll 8
-        for (int jj = 0; jj < 32; jj++) {
-            const int j = 2 * jj + par;
-            const float w = jj < 16 ? __shfl_sync(0xffffffffu, w0, j & 31) : __shfl_sync(0xffffffffu, w1, j & 31);
-            float f[4];
-            i8x4_to_f32(*reinterpret_cast<const uint32_t *>(vbase + j * kHeadDim), f);
+            for (int nt = 0; nt < 8; nt++) {
+                const uint4 kc = *reinterpret_cast<const uint4 *>(blk + (nt * 8 + gid) * kHeadDim + tig * 16);
+                int d[4] = {0, 0, 0, 0};
+                mma_s8_m16n8k32(d, qv.x, qv.x, qv.y, qv.y, kc.x, kc.y);
+                mma_s8_m16n8k32(d, qv.z, qv.z, qv.w, qv.w, kc.z, kc.w);
+                if (nt == gid) dot0 = d[0], dot1 = d[1];  // lane L keeps positions 2L, 2L+1
+            }
+            const int p0 = 2 * lane, p1 = p0 + 1;
+            const float2 ks = *reinterpret_cast<const float2 *>(blk + kKScaleOffset + 8 * lane);
+            const float s0 = p0 < valid ? __fmul_rn(__fmul_rn(__int2float_rn(dot0), ks.x), scale) : -INFINITY;
+            const float s1 = p1 < valid ? __fmul_rn(__fmul_rn(__int2float_rn(dot1), ks.y), scale) : -INFINITY;
+            const float m_new = fmaxf(m, warp_max_f(fmaxf(s0, s1)));
+            const float e0 = p0 < valid ? expf(s0 - m_new) : 0.0f;
+            const float e1 = p1 < valid ? expf(s1 - m_new) : 0.0f;
+            const float corr = expf(m - m_new);
+            l = l * corr + warp_sum_f(e0 + e1);
+            m = m_new;
+            const float2 vs = *reinterpret_cast<const float2 *>(blk + kVScaleOffset + 8 * lane);
+            const float w0 = p0 < valid ? e0 * vs.x : 0.0f;
+            const float w1 = p1 < valid ? e1 * vs.y : 0.0f;
+            // power-of-two range guard: w' = w * 2^e < 2^12
+            int ex;
+            frexpf(warp_max_f(fmaxf(w0, w1)), &ex);
+            const int e_page = 12 - max(0, ex);
+            const float rescale = corr * exp2f((float)(e_page - e_acc));
+            e_acc = e_page;
+            const float f = exp2f((float)e_page);
+            const float x0 = w0 * f, x1 = w1 * f;
+            const float h0 = __half2float(__float2half_rn(x0)), h1 = __half2float(__float2half_rn(x1));
+            const uint32_t H = pack_h2(h0, h1);
+            const uint32_t Lo = pack_h2(x0 - h0, x1 - h1);
 #pragma unroll
-            for (int i = 0; i < 4; i++) o[i] = fmaf(w, f[i], o[i]);
+            for (int nt = 0; nt < 8; nt++)
+#pragma unroll
+                for (int i = 0; i < 4; i++) acc[nt][i] *= rescale;
+            // ---- PV ----
+            uint32_t A0[4], A2[4];  // row gid (0 = hi, 1 = lo) of the four k-steps
+#pragma unroll
+            for (int ks_ = 0; ks_ < 4; ks_++) {
+                const uint32_t ha = __shfl_sync(0xffffffffu, H, 8 * ks_ + tig);
+                const uint32_t la = __shfl_sync(0xffffffffu, Lo, 8 * ks_ + tig);
+                const uint32_t hb = __shfl_sync(0xffffffffu, H, 8 * ks_ + 4 + tig);
+                const uint32_t lb = __shfl_sync(0xffffffffu, Lo, 8 * ks_ + 4 + tig);
+                A0[ks_] = gid == 0 ? ha : (gid == 1 ? la : 0u);
+                A2[ks_] = gid == 0 ? hb : (gid == 1 ? lb : 0u);
+            }
+            const uint8_t *vt = blk + kVOffset;
+#pragma unroll
+            for (int nt = 0; nt < 8; nt++) {
+                const uint4 vc = *reinterpret_cast<const uint4 *>(vt + (nt * 8 + gid) * kHeadDim + tig * 16);
+                const uint32_t vw[4] = {vc.x, vc.y, vc.z, vc.w};
+#pragma unroll
+                for (int ks_ = 0; ks_ < 4; ks_++)
+                    mma_f16_m16n8k16(acc[nt], A0[ks_], A2[ks_], u8x2_to_h2(vw[ks_], 0x4140), u8x2_to_h2(vw[ks_], 0x4342));
+            }
+            __syncwarp();
+            consumed++;
+            if (lane == 0 && advance_producer()) issue_one();
         }
-        __syncwarp();
-        if (lane == 0 && it + kAttnStages < n_it) issue(it + kAttnStages);
+        if (timed_out) break;
+        // rows 0 (hi) and 1 (lo) live in lanes 0-3 and 4-7: o = (hi + lo) * 2^-e
+        const float unscale = exp2f((float)(-e_acc));
+        float o[8][2];
+#pragma unroll
+        for (int nt = 0; nt < 8; nt++) {
+            const float lo0 = __shfl_down_sync(0xffffffffu, acc[nt][0], 4);
+            const float lo1 = __shfl_down_sync(0xffffffffu, acc[nt][1], 4);
+            o[nt][0] = (acc[nt][0] + lo0) * unscale;
+            o[nt][1] = (acc[nt][1] + lo1) * unscale;
+        }
+        const size_t rh_index = (size_t)it.row * a.heads + it.head;
+        float *out = a.out + rh_index * kHeadDim;
+        if (it.n_chunks == 1) {
+            const float inv = 1.0f / l;
+            if (lane < 4)
+#pragma unroll
+                for (int nt = 0; nt < 8; nt++)
+                    *reinterpret_cast<float2 *>(out + nt * 8 + 2 * tig) = make_float2(o[nt][0] * inv, o[nt][1] * inv);
+            continue;
+        }
+        float *part = a.partials + (rh_index * a.max_chunks + it.chunk) * kPartialFloats;
+        if (lane < 4)
+#pragma unroll
+            for (int nt = 0; nt < 8; nt++)
+                *reinterpret_cast<float2 *>(part + nt * 8 + 2 * tig) = make_float2(o[nt][0], o[nt][1]);
+        if (lane == 0) {
+            part[64] = m;
+            part[65] = l;
+        }
+        __threadfence();
+        int last = 0;
+        if (lane == 0) last = atomicAdd(&a.arrivals[rh_index], 1) == it.n_chunks - 1;
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (!last) continue;
+        __threadfence();
+        const float *parts = a.partials + rh_index * a.max_chunks * kPartialFloats;
+        const int dd = 2 * lane;  // merge: lane owns dims 2L, 2L+1
+        float peak = -INFINITY;
+        for (int c = 0; c < it.n_chunks; c++) peak = fmaxf(peak, __ldcg(parts + c * kPartialFloats + 64));
+        float total = 0.0f, m0 = 0.0f, m1 = 0.0f;
+        for (int c = 0; c < it.n_chunks; c++) {
+            const float *pc = parts + c * kPartialFloats;
+            const float wgt = expf(__ldcg(pc + 64) - peak);
+            total += wgt * __ldcg(pc + 65);
+            const float2 v = __ldcg(reinterpret_cast<const float2 *>(pc + dd));
+            m0 += wgt * v.x;
+            m1 += wgt * v.y;
+        }
+        const float inv = 1.0f / total;
+        *reinterpret_cast<float2 *>(out + dd) = make_float2(m0 * inv, m1 * inv);
+        if (lane == 0) a.arrivals[rh_index] = 0;  // ready for the next launch
     }
     if (timed_out) {
-        // record, then wait (bounded) for the copies this warp still has in flight
         if (lane == 0 && a.status) atomicOr(a.status, kStatusTimeout);
-        for (int k = it + 1; k < min(n_it, it + kAttnStages); k++)
-            mbar_wait_bounded(&bars[k % kAttnStages], (k / kAttnStages) & 1, kWaitLimit);
-        return;
     }
-#pragma unroll
-    for (int i = 0; i < 4; i++) o[i] += __shfl_xor_sync(0xffffffffu, o[i], 16);
-
-    const size_t rh_index = (size_t)row * a.heads + head;
-    float *out = a.out + rh_index * kHeadDim;
-    if (n_chunks == 1) {
-        const float inv = 1.0f / l;
-        if (lane < 16)
-            *reinterpret_cast<float4 *>(out + dd) = make_float4(o[0] * inv, o[1] * inv, o[2] * inv, o[3] * inv);
-        return;
-    }
-    // split: publish this chunk's partial, the last arrival merges
-    float *part = a.partials + (rh_index * a.max_chunks + chunk) * kPartialFloats;
-    if (lane < 16) *reinterpret_cast<float4 *>(part + dd) = make_float4(o[0], o[1], o[2], o[3]);
-    if (lane == 0) {
-        part[64] = m;
-        part[65] = l;
-    }
-    __threadfence();
-    int last = 0;
-    if (lane == 0) last = atomicAdd(&a.arrivals[rh_index], 1) == n_chunks - 1;
-    last = __shfl_sync(0xffffffffu, last, 0);
-    if (!last) return;
-    __threadfence();
-    const float *parts = a.partials + rh_index * a.max_chunks * kPartialFloats;
-    float peak = -INFINITY;
-    for (int c = 0; c < n_chunks; c++) peak = fmaxf(peak, __ldcg(parts + c * kPartialFloats + 64));
-    float total = 0.0f;
-    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-    for (int c = 0; c < n_chunks; c++) {
-        const float *pc = parts + c * kPartialFloats;
-        const float wgt = expf(__ldcg(pc + 64) - peak);
-        total += wgt * __ldcg(pc + 65);
-        if (lane < 16) {
-            float4 v = __ldcg(reinterpret_cast<const float4 *>(pc + dd));
-            acc[0] += wgt * v.x, acc[1] += wgt * v.y, acc[2] += wgt * v.z, acc[3] += wgt * v.w;
-        }
-    }
-    const float inv = 1.0f / total;
-    if (lane < 16)
-        *reinterpret_cast<float4 *>(out + dd) = make_float4(acc[0] * inv, acc[1] * inv, acc[2] * inv, acc[3] * inv);
-    if (lane == 0) a.arrivals[rh_index] = 0;  // leave the counter ready for the next launch
+    // drain: every issued copy must land before the CTA exits (bounded)
+    for (unsigned k = consumed + (timed_out ? 1u : 0u); k < issued; k++)
+        mbar_wait_bounded(&bars[k % kAttnStages], (k / kAttnStages) & 1, kWaitLimit);
 }
 
 int launch_attn_decode(const AttnArgs &a, cudaStream_t stream) {
     if (a.rows == 0) return NDL_OK;
     static bool configured = false;  // per process; the attribute is per device function
     const int smem = kAttnWarps * kWarpSmem;
+    static int sms = 0;
     if (!configured) {
         cudaError_t e = cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return set_error(NDL_ERR_CUDA, "attention smem attribute: %s", cudaGetErrorString(e));
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
         configured = true;
     }
-    long long items = (long long)a.rows * a.heads * a.max_chunks;
+    const long long items = (long long)a.rows * a.heads * a.max_chunks;
     long long blocks = (items + kAttnWarps - 1) / kAttnWarps;
-    if (blocks > 0x7FFFFFFF) return set_error(NDL_ERR_INVALID_ARG, "attention grid too large");
+    const long long resident = (long long)sms * 2;  // two CTAs per SM fit the shared memory
+    if (blocks > resident) blocks = resident;
     attn_decode_kernel<<<(unsigned)blocks, kAttnWarps * 32, smem, stream>>>(a);
     return check_launch("attn_decode");
 }

@@ -8,6 +8,8 @@ namespace ndl {
 
 int launch_quantize_rows(const float *x, const float *weight, int rows, int cols, int8_t *q, float *scales,
                          cudaStream_t stream);
+// NDL_ERR_UNSUPPORTED when the CTA-per-row kernel cannot take the shape.
+int launch_swiglu_quantize_rows(const float *gu, int rows, int ffn, int8_t *q, float *scales, cudaStream_t stream);
 
 struct MatmulArgs {
     const int8_t *q;
@@ -22,6 +24,7 @@ struct MatmulArgs {
     int32_t *acc;
     long long w_stride, sw_stride, y_stride;
     int batch;
+    int *status;  // nullable: kernels record timeouts here
 };
 
 // RoPE + int8 quantize of q (per head) and k, v (per position and head) into

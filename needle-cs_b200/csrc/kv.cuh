@@ -2,12 +2,18 @@
 //
 // A page holds 64 consecutive positions of one slot for every layer.  Inside
 // a page, the block of (layer, head) is one contiguous 8704-byte record
-//     [K int8 64x64][K scale f32 x64][V int8 64x64][V scale f32 x64]
+//     [K int8 64x64][K scale f32 x64][V^T u8 64x64][V scale f32 x64]
 // so a single 16-byte-aligned bulk copy brings everything attention needs
 // for 64 positions of one head into shared memory.  This replaces the
 // reference's flat per-slot arrays [layer][capacity][kvWidth] + scales
 // (src/Needle/Engine.cs:184-187,220-223) with the same per-(position, head)
-// int8 + fp32-scale contents.
+// int8 + fp32-scale contents, rearranged for the tensor-core fragments:
+//  * K row j (position j) at 64*j, its 64 dims in the order k_slot(d), so a
+//    lane's m16n8k32 B fragments for both k-steps are one 16-byte chunk;
+//  * V transposed, row d at kVOffset + 64*d, positions in the order
+//    v_slot(p) so a lane's m16n8k16 B fragments for all four k-steps are one
+//    16-byte chunk; bytes hold v + 128 (unsigned) for a 2-op fp16 convert.
+// The query vector uses the K dim order too.
 #pragma once
 
 #include <stdint.h>
@@ -20,6 +26,11 @@ constexpr int kKvBlockBytes = 2 * (kPagePositions * kHeadDim + kPagePositions * 
 constexpr int kKScaleOffset = kPagePositions * kHeadDim;                              // 4096
 constexpr int kVOffset = kKScaleOffset + kPagePositions * 4;                          // 4352
 constexpr int kVScaleOffset = kVOffset + kPagePositions * kHeadDim;                   // 8448
+
+__host__ __device__ __forceinline__ int k_slot(int d) { return ((d & 15) >> 2) * 16 + (d >> 4) * 4 + (d & 3); }
+__host__ __device__ __forceinline__ int v_slot(int p) {
+    return ((p & 7) >> 1) * 16 + (p >> 4) * 4 + ((p >> 3) & 1) * 2 + (p & 1);
+}
 
 __host__ __device__ __forceinline__ size_t kv_page_bytes(int layers, int heads) {
     return (size_t)layers * heads * kKvBlockBytes;

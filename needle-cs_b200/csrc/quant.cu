@@ -133,9 +133,105 @@ __global__ void __launch_bounds__(256) quantize_rows_scalar_kernel(const float *
     if (lane == 0) scales[warp] = scale;
 }
 
+// CTA-per-row variant: 128 threads, element float4 i handled by thread
+// i % 128 (coalesced), values kept in registers between the passes.
+// MODE 0 quantize, 1 RMSNorm + quantize, 2 SwiGLU (row = [gate | up]) + quantize.
+constexpr int kRowThreads = 128;
+constexpr int kRowMaxVec = 8;  // float4 per thread: cols <= 4096
+
+template <int MODE>
+__global__ void __launch_bounds__(kRowThreads) row_quantize_kernel(const float *__restrict__ x,
+                                                                   const float *__restrict__ weight, int cols,
+                                                                   int ld_in, int8_t *__restrict__ q,
+                                                                   float *__restrict__ scales) {
+    __shared__ float red[kRowThreads / 32];
+    const int row = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const float4 *in = reinterpret_cast<const float4 *>(x + (size_t)row * ld_in);
+    const int nv = cols >> 2;
+    float4 v[kRowMaxVec];
+#pragma unroll
+    for (int i = 0; i < kRowMaxVec; i++) {
+        const int idx = tid + i * kRowThreads;
+        v[i] = idx < nv ? in[idx] : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    if (MODE == 2) {
+        const float4 *up = in + nv;
+#pragma unroll
+        for (int i = 0; i < kRowMaxVec; i++) {
+            const int idx = tid + i * kRowThreads;
+            if (idx < nv) {
+                const float4 u = up[idx];
+                float *g = reinterpret_cast<float *>(&v[i]);
+                const float *uu = reinterpret_cast<const float *>(&u);
+#pragma unroll
+                for (int e = 0; e < 4; e++) {
+                    const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g[e])));
+                    g[e] = __fmul_rn(__fmul_rn(g[e], sig), uu[e]);
+                }
+            }
+        }
+    }
+    if (MODE == 1) {
+        float ss = 0.0f;
+#pragma unroll
+        for (int i = 0; i < kRowMaxVec; i++) {
+            ss = __fadd_rn(ss, __fmul_rn(v[i].x, v[i].x));
+            ss = __fadd_rn(ss, __fmul_rn(v[i].y, v[i].y));
+            ss = __fadd_rn(ss, __fmul_rn(v[i].z, v[i].z));
+            ss = __fadd_rn(ss, __fmul_rn(v[i].w, v[i].w));
+        }
+        ss = warp_sum(ss);
+        if (lane == 0) red[warp] = ss;
+        __syncthreads();
+        ss = __fadd_rn(__fadd_rn(red[0], red[1]), __fadd_rn(red[2], red[3]));
+        __syncthreads();
+        const float inv_rms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)cols), 1e-6f)));
+        const float4 *wv = reinterpret_cast<const float4 *>(weight);
+#pragma unroll
+        for (int i = 0; i < kRowMaxVec; i++) {
+            const int idx = tid + i * kRowThreads;
+            if (idx < nv) {
+                const float4 w = wv[idx];
+                v[i].x = __fmul_rn(__fmul_rn(w.x, v[i].x), inv_rms);
+                v[i].y = __fmul_rn(__fmul_rn(w.y, v[i].y), inv_rms);
+                v[i].z = __fmul_rn(__fmul_rn(w.z, v[i].z), inv_rms);
+                v[i].w = __fmul_rn(__fmul_rn(w.w, v[i].w), inv_rms);
+            }
+        }
+    }
+    float peak = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kRowMaxVec; i++)
+        peak = fmaxf(peak, fmaxf(fmaxf(fabsf(v[i].x), fabsf(v[i].y)), fmaxf(fabsf(v[i].z), fabsf(v[i].w))));
+    peak = warp_max(peak);
+    if (lane == 0) red[warp] = peak;
+    __syncthreads();
+    peak = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+    float scale, inverse;
+    scale_from_peak(peak, scale, inverse);
+    uint32_t *out = reinterpret_cast<uint32_t *>(q + (size_t)row * cols);
+#pragma unroll
+    for (int i = 0; i < kRowMaxVec; i++) {
+        const int idx = tid + i * kRowThreads;
+        if (idx < nv) {
+            const uint32_t b0 = (uint8_t)quantize_one(v[i].x, inverse), b1 = (uint8_t)quantize_one(v[i].y, inverse);
+            const uint32_t b2 = (uint8_t)quantize_one(v[i].z, inverse), b3 = (uint8_t)quantize_one(v[i].w, inverse);
+            out[idx] = b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
+        }
+    }
+    if (tid == 0) scales[row] = scale;
+}
+
 int launch_quantize_rows(const float *x, const float *weight, int rows, int cols, int8_t *q, float *scales,
                          cudaStream_t stream) {
     if (rows == 0) return NDL_OK;
+    const bool row_path = (cols % 4 == 0) && cols <= 4 * kRowThreads * kRowMaxVec && aligned(x, 16) &&
+                          aligned(q, 4) && (!weight || aligned(weight, 16));
+    if (row_path) {
+        if (weight) row_quantize_kernel<1><<<rows, kRowThreads, 0, stream>>>(x, weight, cols, cols, q, scales);
+        else row_quantize_kernel<0><<<rows, kRowThreads, 0, stream>>>(x, nullptr, cols, cols, q, scales);
+        return check_launch("row_quantize");
+    }
     dim3 block(256);
     dim3 grid((rows + 7) / 8);
     bool vec = (cols % 16 == 0) && aligned(x, 16) && aligned(q, 16) && (!weight || aligned(weight, 16));
@@ -147,6 +243,16 @@ int launch_quantize_rows(const float *x, const float *weight, int rows, int cols
         else quantize_rows_scalar_kernel<0><<<grid, block, 0, stream>>>(x, nullptr, rows, cols, q, scales);
     }
     return check_launch("quantize_rows");
+}
+
+// SwiGLU of rows [gate (ffn) | up (ffn)] then quantize; falls back to the
+// warp-per-row kernel in step_kernels.cu for shapes the row path cannot hold.
+int launch_swiglu_quantize_rows(const float *gu, int rows, int ffn, int8_t *q, float *scales, cudaStream_t stream) {
+    if (rows == 0) return NDL_OK;
+    if (ffn % 4 != 0 || ffn > 4 * kRowThreads * kRowMaxVec || !aligned(gu, 16) || !aligned(q, 4))
+        return NDL_ERR_UNSUPPORTED;
+    row_quantize_kernel<2><<<rows, kRowThreads, 0, stream>>>(gu, nullptr, ffn, 2 * ffn, q, scales);
+    return check_launch("swiglu_quantize");
 }
 
 }  // namespace ndl

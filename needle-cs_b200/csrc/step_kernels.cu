@@ -78,6 +78,8 @@ __global__ void __launch_bounds__(256) swiglu_quantize_kernel(const float *__res
 int launch_swiglu_quantize(const float *gu, int rows, int ffn, float *act, int8_t *q, float *scales,
                            cudaStream_t stream) {
     if (rows == 0) return NDL_OK;
+    int st = launch_swiglu_quantize_rows(gu, rows, ffn, q, scales, stream);
+    if (st != NDL_ERR_UNSUPPORTED) return st;
     swiglu_quantize_kernel<<<(rows + 7) / 8, 256, 0, stream>>>(gu, rows, ffn, act, q, scales);
     return check_launch("swiglu_quantize");
 }
@@ -284,10 +286,16 @@ __global__ void __launch_bounds__(256) kv_fill_kernel(uint64_t key, int layers, 
     const int8_t q1 = (int8_t)(int)fminf(fmaxf(rintf(__fmul_rn(hi, inverse)), -128.0f), 127.0f);
     const int page = page_row[pos / kPagePositions];
     const int j = pos % kPagePositions;
-    uint8_t *blk = pool + (size_t)page * page_bytes + kv_block_offset(layer, head, heads) + (kind ? kVOffset : 0);
-    blk[j * kHeadDim + lane] = (uint8_t)q0;
-    blk[j * kHeadDim + lane + 32] = (uint8_t)q1;
-    if (lane == 0) reinterpret_cast<float *>(blk + (kind ? (kVScaleOffset - kVOffset) : kKScaleOffset))[j] = scale;
+    uint8_t *blk = pool + (size_t)page * page_bytes + kv_block_offset(layer, head, heads);
+    if (kind == 0) {
+        blk[j * kHeadDim + k_slot(lane)] = (uint8_t)q0;
+        blk[j * kHeadDim + k_slot(lane + 32)] = (uint8_t)q1;
+        if (lane == 0) reinterpret_cast<float *>(blk + kKScaleOffset)[j] = scale;
+    } else {
+        blk[kVOffset + lane * kHeadDim + v_slot(j)] = (uint8_t)(q0 + 128);
+        blk[kVOffset + (lane + 32) * kHeadDim + v_slot(j)] = (uint8_t)(q1 + 128);
+        if (lane == 0) reinterpret_cast<float *>(blk + kVScaleOffset)[j] = scale;
+    }
 }
 
 int launch_kv_fill(uint64_t seed, uint64_t session, int layers, int heads, int first, int count,

@@ -34,29 +34,45 @@ def prefix_kv(ops, oracle, decoder, kv, count, seed, session):
             kv[scales][layer, :count] = s.reshape(count, H)
 
 
+def k_slot(d):
+    return ((d & 15) >> 2) * 16 + (d >> 4) * 4 + (d & 3)
+
+
+def v_slot(p):
+    return ((p & 7) >> 1) * 16 + (p >> 4) * 4 + ((p >> 3) & 1) * 2 + (p & 1)
+
+
+K_ORDER = np.array([k_slot(d) for d in range(64)])  # storage byte of dim d in a K row
+V_ORDER = np.array([v_slot(p) for p in range(64)])  # storage byte of position p in a V^T row
+
+
 def read_slot_kv(engine, slot, positions):
     """Reads positions [0, positions) of a slot from the paged pool into the
-    flat reference layout (k, v int8 [layers][positions][H*64]; ks, vs)."""
+    flat reference layout (k, v int8 [layers][positions][H*64]; ks, vs).
+    Page record of (layer, head): K rows with dims in K_ORDER, K scales,
+    V transposed (row = dim) with positions in V_ORDER holding v + 128, V scales."""
     cfg = engine.model
     H, L = cfg.heads, cfg.layers
     page_bytes = engine.page_bytes()
-    pool_ptr, pool_bytes = engine.tensor_bytes("kv_pool")
     n_pages = (positions + 63) // 64
     pages = [engine.slot_page(slot, i) for i in range(n_pages)]
     need = (max(pages) + 1) * page_bytes
     pool = engine.read_tensor("kv_pool", np.uint8, count=need)
     out = {"k": np.zeros((L, positions, H * 64), np.int8), "v": np.zeros((L, positions, H * 64), np.int8),
            "ks": np.zeros((L, positions, H), np.float32), "vs": np.zeros((L, positions, H), np.float32)}
-    for p in range(positions):
-        page = pages[p // 64]
-        j = p % 64
+    for pi, page in enumerate(pages):
+        lo, hi = pi * 64, min(positions, pi * 64 + 64)
+        n = hi - lo
         for l in range(L):
             for h in range(H):
                 blk = pool[page * page_bytes + (l * H + h) * 8704:][:8704]
-                out["k"][l, p, h * 64:(h + 1) * 64] = blk[j * 64:(j + 1) * 64].view(np.int8)
-                out["ks"][l, p, h] = blk[4096 + 4 * j:4096 + 4 * j + 4].view(np.float32)[0]
-                out["v"][l, p, h * 64:(h + 1) * 64] = blk[4352 + j * 64:4352 + (j + 1) * 64].view(np.int8)
-                out["vs"][l, p, h] = blk[8448 + 4 * j:8448 + 4 * j + 4].view(np.float32)[0]
+                krows = blk[:4096].reshape(64, 64)[:n]
+                out["k"][l, lo:hi, h * 64:(h + 1) * 64] = krows[:, K_ORDER].view(np.int8)
+                out["ks"][l, lo:hi, h] = blk[4096:4352].view(np.float32)[:n]
+                vt = blk[4352:8448].reshape(64, 64)  # [dim][slot]
+                v = (vt[:, V_ORDER[:n]].astype(np.int16) - 128).astype(np.int8)  # [dim][position]
+                out["v"][l, lo:hi, h * 64:(h + 1) * 64] = v.T
+                out["vs"][l, lo:hi, h] = blk[8448:8704].view(np.float32)[:n]
     return out
 
 

@@ -63,6 +63,28 @@ def test_matmul_i8g32_bit_exact(ops, oracle, cuda, m, n, k):
     assert np.array_equal(y.cpu().numpy(), y_ref)
 
 
+@pytest.mark.parametrize("m,n,k", [(64, 2048, 512), (128, 1536, 512), (200, 512, 2048), (512, 4096, 512),
+                                   (100, 96, 96), (129, 136, 160), (512, 8192, 512), (64, 8, 32)])
+def test_matmul_tcgen05_bit_exact(ops, oracle, cuda, m, n, k):
+    """m >= 64 runs the tcgen05 kind::i8 GEMM: D and y identical to the oracle
+    and to the GEMV (batch invariance across the two kernels)."""
+    x, w, sw = _inputs(ops, m, n, k, seed=11)
+    q_ref, s_ref = oracle.quantize_rows(x)
+    y_ref, acc_ref = oracle.matmul_i8g32(q_ref, s_ref, w, sw, want_acc=True)
+    q = torch.from_numpy(q_ref).to(cuda)
+    s = torch.from_numpy(s_ref).to(cuda)
+    wd, swd = torch.from_numpy(w).to(cuda), torch.from_numpy(sw.view(np.int16)).to(cuda)
+    acc = torch.empty((m, n, k // 32), dtype=torch.int32, device=cuda)
+    y = ops.matmul_i8g32(q, s, wd, swd, acc=acc)
+    torch.cuda.synchronize()
+    assert np.array_equal(acc.cpu().numpy(), acc_ref)
+    assert np.array_equal(y.cpu().numpy(), y_ref)
+    # the first 16 rows through the GEMV give the same bits
+    y16 = ops.matmul_i8g32(q[:16].contiguous(), s[:16].contiguous(), wd, swd)
+    torch.cuda.synchronize()
+    assert np.array_equal(y16.cpu().numpy(), y[:16].cpu().numpy())
+
+
 def test_matmul_residual_and_ldy(ops, oracle, cuda):
     m, n, k = 4, 96, 256
     x, w, sw = _inputs(ops, m, n, k, seed=9)
