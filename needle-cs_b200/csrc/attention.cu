@@ -12,9 +12,11 @@
 // cp.async.bulk (3-stage ring, mbarrier completion, bounded waits).  Scores
 // are exact int8 dots (mma.sync s8) scaled by ks * (qs / sqrt(d)); softmax
 // is online (running max, rescaled sum) in fp32 with expf; V is accumulated
-// in fp32 by mma.sync f16 with hi/lo-split probability weights.  A row split into several chunks
-// writes (peak, sum, unnormalised output) partials and the last chunk to
-// finish merges them with exp(peak - max) weights, like MergePartials.
+// in fp32 by mma.sync f16 with hi/lo-split probability weights.  A row
+// longer than one chunk (a fixed number of pages, so the split depends only
+// on the row's own length) writes (peak, sum, unnormalised output) partials
+// that attn_merge_kernel combines with exp(peak - max) weights, like
+// MergePartials.
 #include "common.cuh"
 #include "kernels.cuh"
 #include "kv.cuh"
@@ -115,15 +117,6 @@ constexpr int kAttnStages = 3;
 constexpr int kWarpSmem = kAttnStages * kKvBlockBytes + 64;  // ring + barriers
 constexpr uint32_t kWaitLimit = 1u << 22;
 
-// int8x4 -> 4 floats exactly: bias each byte by 128, splice it under the
-// exponent of 2^23 and subtract 2^23 + 128.
-__device__ __forceinline__ void i8x4_to_f32(uint32_t v, float (&f)[4]) {
-    uint32_t u = v ^ 0x80808080u;
-    f[0] = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7540)) - 8388736.0f;
-    f[1] = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7541)) - 8388736.0f;
-    f[2] = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7542)) - 8388736.0f;
-    f[3] = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7543)) - 8388736.0f;
-}
 
 // Work item i = (row in LPT order, head, chunk) with chunk innermost.
 struct AttnItem {
@@ -199,16 +192,21 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(AttnArgs a
     }
     __syncwarp();
 
+    // Items are dealt in a snake order over rows sorted longest first: round
+    // r gives warp w the item r*W + w (even r) or r*W + W-1-w (odd r).
+    const int wg = blockIdx.x * kAttnWarps + warp;
+    auto item_of = [&](int round) { return round * W + ((round & 1) ? W - 1 - wg : wg); };
     // producer cursor (lane 0): next page to issue
-    int p_item = blockIdx.x * kAttnWarps + warp - W;
+    int p_round = -1;
     AttnItem pit{};
     int p_page = 0, p_left = 0;
     unsigned issued = 0;
     auto advance_producer = [&]() -> bool {
         while (p_left == 0) {
-            p_item += W;
-            if (p_item >= n_items) return false;
-            if (attn_item(a, p_item, pit)) {
+            p_round++;
+            if (p_round * W >= n_items) return false;
+            const int i = item_of(p_round);
+            if (i < n_items && attn_item(a, i, pit)) {
                 p_page = pit.first_page;
                 p_left = pit.n_pages;
             }
@@ -236,9 +234,10 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(AttnArgs a
 
     unsigned consumed = 0;
     bool timed_out = false;
-    for (int item = blockIdx.x * kAttnWarps + warp; item < n_items && !timed_out; item += W) {
+    for (int round = 0; round * W < n_items && !timed_out; round++) {
+        const int item = item_of(round);
         AttnItem it;
-        if (!attn_item(a, item, it)) continue;
+        if (item >= n_items || !attn_item(a, item, it)) continue;
         // query (K dim order): chunk tig = words for both k-steps
         const uint4 qv = __ldg(reinterpret_cast<const uint4 *>(a.q + ((size_t)it.row * a.heads + it.head) * kHeadDim) +
                                tig);
@@ -339,6 +338,8 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(AttnArgs a
                     *reinterpret_cast<float2 *>(out + nt * 8 + 2 * tig) = make_float2(o[nt][0] * inv, o[nt][1] * inv);
             continue;
         }
+        // long row: publish this chunk's (unnormalised output, peak, sum);
+        // attn_merge_kernel combines them after this launch
         float *part = a.partials + (rh_index * a.max_chunks + it.chunk) * kPartialFloats;
         if (lane < 4)
 #pragma unroll
@@ -348,28 +349,6 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(AttnArgs a
             part[64] = m;
             part[65] = l;
         }
-        __threadfence();
-        int last = 0;
-        if (lane == 0) last = atomicAdd(&a.arrivals[rh_index], 1) == it.n_chunks - 1;
-        last = __shfl_sync(0xffffffffu, last, 0);
-        if (!last) continue;
-        __threadfence();
-        const float *parts = a.partials + rh_index * a.max_chunks * kPartialFloats;
-        const int dd = 2 * lane;  // merge: lane owns dims 2L, 2L+1
-        float peak = -INFINITY;
-        for (int c = 0; c < it.n_chunks; c++) peak = fmaxf(peak, __ldcg(parts + c * kPartialFloats + 64));
-        float total = 0.0f, m0 = 0.0f, m1 = 0.0f;
-        for (int c = 0; c < it.n_chunks; c++) {
-            const float *pc = parts + c * kPartialFloats;
-            const float wgt = expf(__ldcg(pc + 64) - peak);
-            total += wgt * __ldcg(pc + 65);
-            const float2 v = __ldcg(reinterpret_cast<const float2 *>(pc + dd));
-            m0 += wgt * v.x;
-            m1 += wgt * v.y;
-        }
-        const float inv = 1.0f / total;
-        *reinterpret_cast<float2 *>(out + dd) = make_float2(m0 * inv, m1 * inv);
-        if (lane == 0) a.arrivals[rh_index] = 0;  // ready for the next launch
     }
     if (timed_out) {
         if (lane == 0 && a.status) atomicOr(a.status, kStatusTimeout);
@@ -377,6 +356,34 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(AttnArgs a
     // drain: every issued copy must land before the CTA exits (bounded)
     for (unsigned k = consumed + (timed_out ? 1u : 0u); k < issued; k++)
         mbar_wait_bounded(&bars[k % kAttnStages], (k / kAttnStages) & 1, kWaitLimit);
+}
+
+// Combines the chunks of every long row (Attention.MergePartials,
+// src/Needle/Blocks.cs:750-817): out = sum_c w_c o_c / sum_c w_c l_c with
+// w_c = exp(peak_c - max peak), chunks in ascending order.  Warp per
+// (row, head); lane owns dims 2*lane, 2*lane+1.
+__global__ void __launch_bounds__(256) attn_merge_kernel(AttnArgs a) {
+    const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (w >= a.rows * a.heads) return;
+    const int row = w / a.heads;
+    const int len = a.row_pos[row] + 1;
+    const int pages = (len + kPagePositions - 1) / kPagePositions;
+    const int n_chunks = (pages + a.chunk_pages - 1) / a.chunk_pages;
+    if (n_chunks < 2) return;
+    const float *parts = a.partials + (size_t)w * a.max_chunks * kPartialFloats;
+    float peak = -INFINITY;
+    for (int c = 0; c < n_chunks; c++) peak = fmaxf(peak, parts[c * kPartialFloats + 64]);
+    float total = 0.0f, m0 = 0.0f, m1 = 0.0f;
+    for (int c = 0; c < n_chunks; c++) {
+        const float *pc = parts + c * kPartialFloats;
+        const float wgt = expf(pc[64] - peak);
+        total += wgt * pc[65];
+        const float2 v = *reinterpret_cast<const float2 *>(pc + 2 * lane);
+        m0 += wgt * v.x;
+        m1 += wgt * v.y;
+    }
+    const float inv = 1.0f / total;
+    *reinterpret_cast<float2 *>(a.out + (size_t)w * kHeadDim + 2 * lane) = make_float2(m0 * inv, m1 * inv);
 }
 
 int launch_attn_decode(const AttnArgs &a, cudaStream_t stream) {
@@ -393,11 +400,16 @@ int launch_attn_decode(const AttnArgs &a, cudaStream_t stream) {
         configured = true;
     }
     const long long items = (long long)a.rows * a.heads * a.max_chunks;
+    if (items > 0x7FFFFFFF) return set_error(NDL_ERR_INVALID_ARG, "attention: too many work items");
     long long blocks = (items + kAttnWarps - 1) / kAttnWarps;
     const long long resident = (long long)sms * 2;  // two CTAs per SM fit the shared memory
     if (blocks > resident) blocks = resident;
     attn_decode_kernel<<<(unsigned)blocks, kAttnWarps * 32, smem, stream>>>(a);
-    return check_launch("attn_decode");
+    int st = check_launch("attn_decode");
+    if (st != NDL_OK || a.max_chunks < 2) return st;
+    const int warps = a.rows * a.heads;
+    attn_merge_kernel<<<(warps + 7) / 8, 256, 0, stream>>>(a);
+    return check_launch("attn_merge");
 }
 
 }  // namespace ndl

@@ -42,7 +42,7 @@ enum : uint64_t {
     kStreamFinalNorm = 2,
     kStreamLayerBase = 100,  // + 16 * layer + field
 };
-constexpr int kAttnChunkPages = 2;  // pages per attention work item
+constexpr int kAttnChunkPages = 8;  // pages per attention work item (512 positions)
 enum : int { kFQkvW, kFQkvS, kFOW, kFOS, kFGuW, kFGuS, kFDW, kFDS, kFAttnNorm, kFFfnNorm };
 
 struct DeviceLayer {

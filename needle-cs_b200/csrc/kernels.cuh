@@ -62,7 +62,7 @@ struct AttnArgs {
     float inv_sqrt_d;
     float *out;       // [rows][heads][64]
     float *partials;  // [rows][heads][max_chunks][kPartialFloats]
-    int *arrivals;    // [rows][heads], zero on entry and on exit
+    int *arrivals;    // unused (kept for layout stability)
     int *status;
 };
 int launch_attn_decode(const AttnArgs &a, cudaStream_t stream);

@@ -178,3 +178,27 @@ def test_host_generation_matches_device(small):
     assert np.array_equal(small.read_tensor("embedding", np.uint16), emb)
     assert np.array_equal(small.read_tensor("w_head", np.int8), wh)
     assert np.array_equal(small.read_tensor("s_head", np.uint16), sh)
+
+
+def test_decode_long_sessions_eight_heads(pkg, ops, oracle, cuda):
+    """The benchmark geometry (8 heads x 64, d 512) with long ragged sessions:
+    attention splits into many 2-page chunks and merges them."""
+    import importlib
+
+    eng_mod = importlib.import_module("needle_cs_b200.engine")
+    model = eng_mod.SyntheticDecoder(layers=2, dim=512, heads=8, head_dim=64, ffn=512, vocab=2048, seed=21)
+    prefix = [300, 1000, 64, 777]
+    with eng_mod.BatchedEngine(model, slots=4, context_length=1088, chunk_size=8) as eng:
+        for s, n in enumerate(prefix):
+            eng.fill_synthetic(s, n, 9, 500 + s)
+        tokens = [17, 1999, 3, 1024]
+        eng.forward_batch(tokens, [0, 1, 2, 3], [0, 1, 2, 3])
+        ids = eng.sample_argmax()
+        dec = oracle_decoder(oracle, eng)
+        for s, n in enumerate(prefix):
+            kv = dec.new_kv()
+            prefix_kv(ops, oracle, dec, kv, n, 9, 500 + s)
+            ref = dec.row(tokens[s], n, kv)
+            ok, err = logits_close(eng.batch_logits_row(s), ref)
+            assert ok, f"slot {s}: max err {err}"
+            assert ids[s] == int(np.argmax(ref)), f"slot {s}: margin {top2_margin(ref)}"
