@@ -119,14 +119,15 @@ NDL_API int ndl_rmsnorm_quantize(const float *x, const float *weight, int rows, 
 
 /* I8G32 quantized linear.  Replaces Quant.MatMulRows
  * (src/Needle/Quant.cs:615-633 -> src/Needle/Gemv.cs:117-333; scalar
- * definition src/Needle/Scalar.cs:146-192) for int8 weights with one fp16
- * scale per (row, 32-column group):
- *   D[t][n][g] = sum_{k in g} w[n][k]*q[t][k]            (int32, exact)
- *   y[t][n]    = (residual ? residual[t][n] : 0) + sum_g (half(sw[n][g]) * sa[t]) * float(D)
- * with g ascending and no fused multiply-add, so y is bit-identical to the
- * scalar definition whatever the batch size.  acc (nullable) receives D as
- * [m][n][k/32].  k must be a multiple of 32; w, q 16-byte aligned.
- * M < 64 runs the streaming GEMV; M >= 64 the tcgen05 kind::i8 GEMM. */
+ * skeleton src/Needle/Scalar.cs:146-192) for int8 weights with one fp16
+ * scale per (row, 32-column group) and one activation scale per row:
+ *   D[t][n][g] = sum_{k in g} w[n][k]*q[t][k]              (int32, exact)
+ *   acc        = fma(half(sw[n][g]), float(D), acc)         (g ascending)
+ *   y[t][n]    = (residual ? residual[t][n] : 0) + acc * sa[t]
+ * The same operation order in every kernel, so y is bit-identical across
+ * batch sizes and kernels.  acc (nullable) receives D as [m][n][k/32].
+ * k must be a multiple of 32; w, q 16-byte aligned.  Small m runs the
+ * streaming GEMV (mma.sync); packed batches the tcgen05 kind::i8 GEMM. */
 NDL_API int ndl_matmul_i8g32(const int8_t *q, const float *sa, int m, const int8_t *w, const uint16_t *sw, int n,
                              int k, float *y, int ldy, const float *residual, int32_t *acc, void *stream);
 

@@ -1,24 +1,26 @@
 // I8G32 GEMM on the 5th-generation tensor cores for packed batches (m >= 64).
 //
-// Same result as the streaming GEMV and the scalar definition
-// (Scalar.MatMulRows skeleton, src/Needle/Scalar.cs:146-192, with raw int8
-// weights and 32-column groups), bit for bit:
-//   y[t][n] = (residual) + sum_g (half(sw[n][g]) * sa[t]) * float(D[t][n][g])
+// Same result as the streaming GEMV and the oracle (Scalar.MatMulRows
+// skeleton, src/Needle/Scalar.cs:146-192, with raw int8 weights, 32-column
+// groups and the per-row activation scale factored out), bit for bit:
+//   y[t][n] = (residual) + sa[t] * (fma over g ascending of half(sw[n][g]) * D[t][n][g])
 //
-// One CTA computes a 128 x BN output tile (BN = 64, or 32 when 64 would
-// leave SMs without a tile); two CTAs fit on an SM.
+// One CTA computes a 128 x BN output tile (BN = 32, or 16 when 32 would
+// leave fewer than two tiles per SM); two CTAs fit on an SM.
 //  * warp 0 (one lane): TMA loads of the activation tile A [128 rows][128 B]
 //    and the weight tile B [BN rows][128 B] per stage, 128-byte swizzle,
 //    3- or 4-stage ring (no cluster multicast).
-//  * warp 1: allocates 4*BN TMEM columns; one lane issues one
+//  * warp 1: allocates 8*BN TMEM columns; one lane issues one
 //    tcgen05.mma kind::i8 (M 128, N BN, K 32) per 32-column group, with
-//    accumulate off, into one of four BN-column TMEM buffers.  Each MMA's
-//    int32 result is therefore exactly D of that group.
-//  * warps 2..: epilogue, one per (TMEM lane quadrant, 32 columns).  Thread
-//    (warp w, lane l) owns output row 32*(w%4)+l; for every group in
-//    ascending order it reads
-//    D from TMEM, releases the buffer, and folds
-//    acc += (sw * sa) * float(D) with round-to-nearest multiplies and adds.
+//    accumulate off, into its own BN-column accumulator: the four groups of
+//    a stage fill one of two TMEM slots.  Each MMA's int32 result is
+//    therefore exactly D of that group.
+//  * warps 2..: epilogue, one per (TMEM lane quadrant, 16 columns).  Thread
+//    (warp w, lane l) owns output row 32*(w%4)+l; per slot it reads the four
+//    groups' D from TMEM, releases the slot, and for every group in
+//    ascending order folds
+//    acc = fma(sw, float(D), acc); the row's activation scale multiplies
+//    the result once at the end.
 // Every wait is bounded; on a timeout the CTA records kStatusTimeout,
 // drains, frees TMEM and exits.
 #include <cudaTypedefs.h>
@@ -36,11 +38,11 @@ constexpr int kTcMaxGroups = 64;  // k <= 2048
 constexpr int kTcATileBytes = kTcBlockM * kTcBlockK;  // 16 KB
 constexpr uint32_t kTcWaitLimit = 1u << 26;
 
-// BN = 32 or 64 output columns per CTA (two CTAs per SM fit); one epilogue
-// warp per (TMEM lane quadrant, 32 columns).
+// BN = 16 or 32 output columns per CTA (two CTAs per SM fit); one epilogue
+// warp per (TMEM lane quadrant, 16 columns).
 template <int BN>
 constexpr int tc_stages() {
-    return BN == 64 ? 3 : 4;  // ~90 KB of shared memory either way: two CTAs per SM
+    return 4;  // about 76 KB (BN 16) or 88 KB (BN 32): two CTAs per SM
 }
 
 template <int BN>
@@ -56,7 +58,7 @@ struct TcSmem {
 
 template <int BN>
 __host__ __device__ constexpr int tc_threads() {
-    return 64 + 4 * BN;  // 2 control warps + (BN / 32) * 4 epilogue warps
+    return 64 + 8 * BN;  // 2 control warps + (BN / 16) * 4 epilogue warps
 }
 
 struct TcParams {
@@ -82,8 +84,9 @@ __global__ void __launch_bounds__(tc_threads<BN>(), 2)
     gemm_i8g32_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                          TcParams p) {
     constexpr int kThreads = tc_threads<BN>();
-    constexpr int kEpiWarps = 4 * (BN / 32);
-    constexpr uint32_t kTmemCols = kTcAccBufs * BN;  // 128 or 256: a power of two
+    constexpr int kEpiWarps = 4 * (BN / 16);
+    constexpr int kSlotCols = 4 * BN;                 // one smem stage = 4 groups = 4 accumulators
+    constexpr uint32_t kTmemCols = kTcAccBufs / 2 * kSlotCols;  // two slots: 128 (BN 16) or 256 (BN 32)
     constexpr int kBTileBytes = BN * kTcBlockK;
     constexpr int kTcStages = TcSmem<BN>::kStages;
     extern __shared__ uint8_t smem_raw[];
@@ -96,7 +99,7 @@ __global__ void __launch_bounds__(tc_threads<BN>(), 2)
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < kTcStages; i++) mbar_init(&s.full[i], 1), mbar_init(&s.empty[i], 1);
-        for (int i = 0; i < kTcAccBufs; i++) mbar_init(&s.acc_full[i], 1), mbar_init(&s.acc_empty[i], kEpiWarps);
+        for (int i = 0; i < 2; i++) mbar_init(&s.acc_full[i], 1), mbar_init(&s.acc_empty[i], kEpiWarps);
         s.abort = 0;
         fence_mbar_init();
         prefetch_tmap(&map_a);
@@ -105,15 +108,6 @@ __global__ void __launch_bounds__(tc_threads<BN>(), 2)
     if (warp == 1) {
         tmem_alloc(&s.tmem_base, kTmemCols);
         tmem_relinquish();
-    }
-    // decoded scales of this tile: swf[g][nl] = half(sw[n0+nl][g]) (coalesced rows)
-    {
-        const uint16_t *sw = p.sw + (long long)bz * p.sw_stride;
-        for (int i = threadIdx.x; i < BN * G; i += kThreads) {
-            const int nl = i / G, g = i - nl * G;
-            const int n = n0 + nl;
-            s.swf[g][nl] = n < p.n ? half_to_float_ref_fast(sw[(size_t)n * G + g]) : 0.0f;
-        }
     }
     tc_fence_before();
     __syncthreads();
@@ -133,63 +127,99 @@ __global__ void __launch_bounds__(tc_threads<BN>(), 2)
     } else if (warp == 1) {
         if (lane == 0) {
             const uint32_t idesc = idesc_i8(kTcBlockM, BN);
-            for (int g = 0; g < G && !s.abort; g++) {
-                const int st = g >> 2, j = g & 3, slot = st % kTcStages, buf = g % kTcAccBufs;
-                if (j == 0 && !tc_wait(s, &s.full[slot], (st / kTcStages) & 1)) break;
-                if (g >= kTcAccBufs && !tc_wait(s, &s.acc_empty[buf], ((g / kTcAccBufs) - 1) & 1)) break;
+            for (int st = 0; st < n_stages && !s.abort; st++) {
+                const int slot = st % kTcStages, acc = st & 1;
+                if (!tc_wait(s, &s.full[slot], (st / kTcStages) & 1)) break;
+                if (st >= 2 && !tc_wait(s, &s.acc_empty[acc], ((st >> 1) - 1) & 1)) break;
                 tc_fence_after();
-                const uint64_t da = sw128_kmajor_desc(s.a[slot]) + (uint64_t)(j * 2);
-                const uint64_t db = sw128_kmajor_desc(s.b[slot]) + (uint64_t)(j * 2);
-                mma_i8(tmem + (uint32_t)(buf * BN), da, db, idesc, 0u);
-                mma_commit(&s.acc_full[buf]);
-                if (j == 3 || g == G - 1) mma_commit(&s.empty[slot]);
+                const uint64_t da0 = sw128_kmajor_desc(s.a[slot]), db0 = sw128_kmajor_desc(s.b[slot]);
+                const int groups = min(4, G - 4 * st);
+                for (int j = 0; j < groups; j++)
+                    mma_i8(tmem + (uint32_t)(acc * kSlotCols + j * BN), da0 + (uint64_t)(j * 2),
+                           db0 + (uint64_t)(j * 2), idesc, 0u);
+                mma_commit(&s.acc_full[acc]);
+                mma_commit(&s.empty[slot]);
             }
         }
     } else {
-        // epilogue warp: lane quadrant (TMEM lanes 32*quad..), 32 columns at col0
-        const int quad = warp & 3, col0 = ((warp - 2) >> 2) * 32;
+        // epilogue warp: lane quadrant (TMEM lanes 32*quad..), 16 columns at col0
+        const int quad = warp & 3, col0 = ((warp - 2) >> 2) * 16;
+        const int epi = threadIdx.x - 64;
+        // decoded scales of this tile, swf[g][nl] = half(sw[n0+nl][g]), loaded
+        // while the first TMA loads are in flight
+        {
+            const uint16_t *sw = p.sw + (long long)bz * p.sw_stride;
+            for (int i = epi; i < BN * G; i += kThreads - 64) {
+                const int nl = i / G, g = i - nl * G;
+                const int n = n0 + nl;
+                s.swf[g][nl] = n < p.n ? half_to_float_ref_fast(sw[(size_t)n * G + g]) : 0.0f;
+            }
+            asm volatile("bar.sync 1, %0;" ::"r"(kThreads - 64) : "memory");
+        }
         const int t = m0 + quad * 32 + lane;
         const bool tv = t < p.m;
-        const float sa = tv ? p.sa[t] : 0.0f;
-        float acc[32];
+        float acc[16];
 #pragma unroll
-        for (int j = 0; j < 32; j++) acc[j] = 0.0f;
+        for (int j = 0; j < 16; j++) acc[j] = 0.0f;
         const uint32_t lane_addr = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)col0;
-        for (int g = 0; g < G; g++) {
-            const int buf = g % kTcAccBufs;
-            if (!tc_wait(s, &s.acc_full[buf], (g / kTcAccBufs) & 1)) break;
+        for (int st = 0; st < n_stages; st++) {
+            const int a = st & 1;
+            if (!tc_wait(s, &s.acc_full[a], (st >> 1) & 1)) break;
             tc_fence_after();
-            uint32_t d[32];
-            tmem_ld32(lane_addr + (uint32_t)(buf * BN), d);
-            tmem_ld_wait();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&s.acc_empty[buf]);
-            const float4 *sc = reinterpret_cast<const float4 *>(&s.swf[g][col0]);
+            const int groups = min(4, G - 4 * st);
+            // two groups at a time (32 registers of D); the slot is released
+            // once all four are in registers
 #pragma unroll
-            for (int q = 0; q < 8; q++) {
-                const float4 w = sc[q];
-                acc[4 * q + 0] = __fadd_rn(acc[4 * q + 0], __fmul_rn(__fmul_rn(w.x, sa), __int_as_float((int)d[4 * q + 0] + 0x4B400000) - 12582912.0f));
-                acc[4 * q + 1] = __fadd_rn(acc[4 * q + 1], __fmul_rn(__fmul_rn(w.y, sa), __int_as_float((int)d[4 * q + 1] + 0x4B400000) - 12582912.0f));
-                acc[4 * q + 2] = __fadd_rn(acc[4 * q + 2], __fmul_rn(__fmul_rn(w.z, sa), __int_as_float((int)d[4 * q + 2] + 0x4B400000) - 12582912.0f));
-                acc[4 * q + 3] = __fadd_rn(acc[4 * q + 3], __fmul_rn(__fmul_rn(w.w, sa), __int_as_float((int)d[4 * q + 3] + 0x4B400000) - 12582912.0f));
-            }
-            if (p.acc && tv) {  // optional int32 accumulator output (parity checks)
-                int32_t *dst = p.acc + ((size_t)t * p.n + n0 + col0) * G + g;
-                const int jmax = min(32, p.n - (n0 + col0));
+            for (int h = 0; h < 2; h++) {
+                uint32_t d[2][16];
 #pragma unroll
-                for (int j = 0; j < 32; j++)
-                    if (j < jmax) dst[(size_t)j * G] = (int)d[j];
+                for (int jj = 0; jj < 2; jj++)
+                    if (2 * h + jj < groups)
+                        tmem_ld16(lane_addr + (uint32_t)(a * kSlotCols + (2 * h + jj) * BN), d[jj]);
+                tmem_ld_wait();
+                if (h == 1) {
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&s.acc_empty[a]);
+                }
+                // acc = fma(sw, float(D), acc) in ascending group order; float(D)
+                // exact by the 1.5*2^23 trick
+#pragma unroll
+                for (int jj = 0; jj < 2; jj++) {
+                    const int j = 2 * h + jj;
+                    if (j >= groups) break;
+                    const int g = 4 * st + j;
+                    const float4 *sc = reinterpret_cast<const float4 *>(&s.swf[g][col0]);
+#pragma unroll
+                    for (int q = 0; q < 4; q++) {
+                        const float4 w = sc[q];
+                        acc[4 * q + 0] = __fmaf_rn(w.x, __int_as_float((int)d[jj][4 * q + 0] + 0x4B400000) - 12582912.0f, acc[4 * q + 0]);
+                        acc[4 * q + 1] = __fmaf_rn(w.y, __int_as_float((int)d[jj][4 * q + 1] + 0x4B400000) - 12582912.0f, acc[4 * q + 1]);
+                        acc[4 * q + 2] = __fmaf_rn(w.z, __int_as_float((int)d[jj][4 * q + 2] + 0x4B400000) - 12582912.0f, acc[4 * q + 2]);
+                        acc[4 * q + 3] = __fmaf_rn(w.w, __int_as_float((int)d[jj][4 * q + 3] + 0x4B400000) - 12582912.0f, acc[4 * q + 3]);
+                    }
+                    if (p.acc && tv) {  // optional int32 accumulator output (parity checks)
+                        int32_t *dst = p.acc + ((size_t)t * p.n + n0 + col0) * G + g;
+                        const int cmax = min(16, p.n - (n0 + col0));
+#pragma unroll
+                        for (int c = 0; c < 16; c++)
+                            if (c < cmax) dst[(size_t)c * G] = (int)d[jj][c];
+                    }
+                }
             }
         }
         if (tv && !s.abort) {
+            const float sa = p.sa[t];
             float *y = p.y + (long long)bz * p.y_stride + (size_t)t * p.ldy;
             const float *res = p.residual ? p.residual + (size_t)t * p.ldy : nullptr;
             const int nb = n0 + col0;
 #pragma unroll
-            for (int j = 0; j < 32; j++) {
+            for (int j = 0; j < 16; j++) {
                 const int n = nb + j;
-                if (n < p.n) y[n] = res ? __fadd_rn(res[n], acc[j]) : acc[j];
+                if (n < p.n) {
+                    const float v = __fmul_rn(acc[j], sa);
+                    y[n] = res ? __fadd_rn(res[n], v) : v;
+                }
             }
         }
     }
@@ -273,15 +303,16 @@ int launch_gemm_i8g32_tc(const MatmulArgs &a, cudaStream_t stream) {
     }
     // widest tile that still covers the SMs (two CTAs per SM fit for BN <= 64)
     const long long mt = (a.m + kTcBlockM - 1) / kTcBlockM * (long long)a.batch;
-    const int bn = mt * ((a.n + 63) / 64) >= sms ? 64 : 32;
+    // 32-column tiles when they still give two tiles per SM, else 16
+    const int bn = mt * ((a.n + 31) / 32) >= 2 * sms ? 32 : 16;
     CUtensorMap map_a, map_b;
     int st = make_map(&map_a, a.q, a.k, a.m, 1, 0);
     if (st != NDL_OK) return st;
     st = make_weight_map(&map_b, a, bn);
     if (st != NDL_OK) return st;
     TcParams p{a.m, a.n, a.k, a.ldy, a.batch, a.sa, a.sw, a.sw_stride, a.y_stride, a.y, a.residual, a.acc, a.status};
-    if (bn == 64) return launch_bn<64>(map_a, map_b, p, a, stream);
-    return launch_bn<32>(map_a, map_b, p, a, stream);
+    if (bn == 32) return launch_bn<32>(map_a, map_b, p, a, stream);
+    return launch_bn<16>(map_a, map_b, p, a, stream);
 }
 
 }  // namespace ndl

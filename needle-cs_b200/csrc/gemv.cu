@@ -1,5 +1,6 @@
-// I8G32 streaming GEMV: y[t][n] = sum_g (half(sw[n][g]) * sa[t]) * D[t][n][g]
-// with D the exact int32 dot over one 32-column group.
+// I8G32 streaming GEMV: y[t][n] = sa[t] * sum_g half(sw[n][g]) * D[t][n][g]
+// with D the exact int32 dot over one 32-column group, the group sum a chain
+// of fused multiply-adds in ascending group order.
 //
 // Replaces Quant.MatMulRows -> Gemv.Rows/Block/Tile4/Tile2
 // (src/Needle/Quant.cs:615-633, src/Needle/Gemv.cs:117-333) for the M < 64
@@ -8,9 +9,10 @@
 //    walks every 32-column group in ascending order.  Each group is one
 //    mma.sync.m16n8k32 (K = 32 = one group), so the int32 accumulator of an
 //    MMA is exactly D for that group; the lane then folds its four (t, n)
-//    results into fp32 accumulators with round-to-nearest multiplies and
-//    adds (no FMA), in group order.  That is the scalar definition bit for
-//    bit, and a row's result does not depend on the batch it is in.
+//    results into fp32 accumulators, acc = fma(sw, D, acc), in group order,
+//    and multiplies by the row's activation scale at the end.  That is the
+//    oracle's definition bit for bit, and a row's result does not depend on
+//    the batch it is in.
 //  * Weight bytes are read once with L1-bypassing 8-byte loads, eight groups
 //    in flight per lane.  The MMA computes sum_k A[t][k] B[k][n] over a
 //    32-wide k slice; any permutation of k applied to both operands leaves
@@ -89,10 +91,10 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_i8g32_kernel(MatmulArgs 
             int d[4];
             mma_s8_16x8x32(d, A0[u].x, A1[u].x, A0[u].y, A1[u].y, B[u].x, B[u].y);
             const float s0 = half_to_float_ref_fast(h0[u]), s1 = half_to_float_ref_fast(h1[u]);
-            acc0 = __fadd_rn(acc0, __fmul_rn(__fmul_rn(s0, sa_a), exact_i2f(d[0])));
-            acc1 = __fadd_rn(acc1, __fmul_rn(__fmul_rn(s1, sa_a), exact_i2f(d[1])));
-            acc2 = __fadd_rn(acc2, __fmul_rn(__fmul_rn(s0, sa_b), exact_i2f(d[2])));
-            acc3 = __fadd_rn(acc3, __fmul_rn(__fmul_rn(s1, sa_b), exact_i2f(d[3])));
+            acc0 = __fmaf_rn(s0, exact_i2f(d[0]), acc0);
+            acc1 = __fmaf_rn(s1, exact_i2f(d[1]), acc1);
+            acc2 = __fmaf_rn(s0, exact_i2f(d[2]), acc2);
+            acc3 = __fmaf_rn(s1, exact_i2f(d[3]), acc3);
             if (a.acc) {
                 const int g = g0 + u;
                 if (va && vc0) a.acc[((size_t)ta * a.n + nc) * G + g] = d[0];
@@ -106,10 +108,10 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_i8g32_kernel(MatmulArgs 
         size_t o = (size_t)t * a.ldy + n;
         y[o] = a.residual ? __fadd_rn(a.residual[o], v) : v;
     };
-    if (va && vc0) store(ta, nc, acc0);
-    if (va && vc1) store(ta, nc + 1, acc1);
-    if (vb && vc0) store(tb, nc, acc2);
-    if (vb && vc1) store(tb, nc + 1, acc3);
+    if (va && vc0) store(ta, nc, __fmul_rn(acc0, sa_a));
+    if (va && vc1) store(ta, nc + 1, __fmul_rn(acc1, sa_a));
+    if (vb && vc0) store(tb, nc, __fmul_rn(acc2, sa_b));
+    if (vb && vc1) store(tb, nc + 1, __fmul_rn(acc3, sa_b));
 }
 
 int launch_gemv_i8g32(const MatmulArgs &a, cudaStream_t stream) {

@@ -329,7 +329,13 @@ void ndo_matmul_rows_cq(const uint8_t *indices, const uint16_t *norms, const ndo
 }
 
 /* I8G32: the Scalar.MatMulRows skeleton (Scalar.cs:146-192) with raw int8
- * weights, 32-column groups and one activation scale per row. */
+ * weights and 32-column groups.  The activation scale is one per row, so it
+ * is factored out of the group sum:
+ *   acc = fmaf(half(sw[n][g]), (float)D[t][n][g], acc)   for g ascending
+ *   y[t][n] = acc * sa[t]
+ * (the per-group fused multiply-add mirrors the reference's SIMD GEMV,
+ * src/Needle/Gemv.cs:259-316, which folds each group's int32 dot into the
+ * float accumulator with an FMA). */
 void ndo_matmul_i8g32(const int8_t *w, const uint16_t *sw, int n_rows, int k, const int8_t *q, const float *sa,
                       int m, int32_t *acc, float *y, int ldy) {
     int groups = k / 32;
@@ -343,10 +349,9 @@ void ndo_matmul_i8g32(const int8_t *w, const uint16_t *sw, int n_rows, int k, co
                 int dot = 0;
                 for (int j = 0; j < 32; j++) dot += row[g * 32 + j] * x[g * 32 + j];
                 if (acc) acc[((size_t)t * n_rows + n) * groups + g] = dot;
-                float scaled = ndo_half_to_single(scales[g]) * sa[t];
-                accumulator += scaled * (float)dot;
+                accumulator = fmaf(ndo_half_to_single(scales[g]), (float)dot, accumulator);
             }
-            y[(size_t)t * ldy + n] = accumulator;
+            y[(size_t)t * ldy + n] = accumulator * sa[t];
         }
     }
 }

@@ -68,8 +68,8 @@ void ndo_matmul_rows_cq(const uint8_t *indices, const uint16_t *norms, const ndo
                         int stride, int tokens, float *y, int ldy, int row_start, int row_end);
 /* I8G32: int8 weights [N][K], fp16 scale per (row, 32-column group).  Same
  * skeleton as Scalar.MatMulRows with a 32-group and raw int8 weights:
- *   D[t][n][g] = sum_{k in g} w[n][k] * q[t][k]              (int32)
- *   y[t][n]    = sum_g (half(sw[n][g]) * sa[t]) * (float)D     (fp32, g ascending)
+ *   D[t][n][g] = sum_{k in g} w[n][k] * q[t][k]                   (int32)
+ *   y[t][n]    = sa[t] * (fma over g ascending of half(sw[n][g]) * D)  (fp32)
  * acc (nullable) receives D as [M][N][K/32]. */
 void ndo_matmul_i8g32(const int8_t *w, const uint16_t *sw, int n_rows, int k, const int8_t *q, const float *sa,
                       int m, int32_t *acc, float *y, int ldy);
