@@ -201,6 +201,9 @@ enum {
     NDL_PROF_CLASSES
 };
 NDL_API int ndl_engine_profile(ndl_engine *e, int enable);
+/* Steps are captured as one CUDA graph per (rows, heads) shape and replayed
+ * (default on; profiling runs the kernels directly). */
+NDL_API int ndl_engine_use_graphs(ndl_engine *e, int enable);
 NDL_API int ndl_engine_profile_read(ndl_engine *e, double *ms, long long *launches, int reset);
 
 /* Slot state: BatchedEngine.SlotLength/ResetSlot/MarkSlot/RewindSlot

@@ -53,6 +53,7 @@ SIGNATURES = {
     "ndl_sample_argmax": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p]),
     "ndl_sample_topk": (c_int, [c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p]),
     "ndl_engine_profile": (c_int, [c_void_p, c_int]),
+    "ndl_engine_use_graphs": (c_int, [c_void_p, c_int]),
     "ndl_engine_profile_read": (c_int, [c_void_p, c_void_p, c_void_p, c_int]),
 }
 

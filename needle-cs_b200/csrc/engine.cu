@@ -23,9 +23,8 @@
 
 namespace ndl {
 
-int launch_step_prepare(const int32_t *updates, int n_updates, int32_t *page_table, int max_pages,
-                        const int32_t *tokens, int rows, const uint16_t *embedding, int vocab, int dim, float *x,
-                        int *status, cudaStream_t stream);
+int launch_step_prepare(const int32_t *updates, int32_t *page_table, int max_pages, const int32_t *tokens, int rows,
+                        const uint16_t *embedding, int vocab, int dim, float *x, int *status, cudaStream_t stream);
 int launch_swiglu_quantize(const float *gu, int rows, int ffn, float *act, int8_t *q, float *scales,
                            cudaStream_t stream);
 int launch_gather_rows(const float *x, const int32_t *idx, int n, int dim, float *out, cudaStream_t stream);
@@ -90,6 +89,15 @@ struct ndl_engine {
     void *h_out = nullptr;  // pinned sampling results
     int last_rows = 0, last_heads = 0;
     int max_chunks_cap = 0;
+    // captured step graphs, keyed by (rows, heads)
+    struct StepGraph {
+        int rows, heads;
+        cudaGraphExec_t exec;
+        unsigned long long last_use;
+    };
+    std::vector<StepGraph> graphs;
+    unsigned long long graph_clock = 0;
+    bool use_graphs = true;
     // per-kernel-class timing (CUDA events on the engine stream)
     bool profile = false;
     std::vector<cudaEvent_t> event_pool;
@@ -333,6 +341,120 @@ int check_slot(ndl_engine *e, int slot) {
     return NDL_OK;
 }
 
+// The device work of one step.  Every kernel reads its per-step data from
+// d_meta, so the sequence can be captured once per (rows, heads) and replayed.
+int step_kernels(ndl_engine *e, int rows, int heads) {
+    const ndl_decoder_config &c = e->dc;
+    cudaStream_t s = e->stream;
+    const int32_t *d_tokens = e->d_meta + e->off_tokens, *d_slot = e->d_meta + e->off_slot;
+    const int32_t *d_pos = e->d_meta + e->off_pos, *d_order = e->d_meta + e->off_order;
+    const int32_t *d_head = e->d_meta + e->off_head;
+    {
+        ProfScope p(e, NDL_PROF_PREPARE);
+        TRY(launch_step_prepare(e->d_meta + e->off_updates, e->d_page_table, e->max_pages, d_tokens, rows,
+                                e->embedding, c.vocab, c.dim, e->x, e->d_status, s));
+    }
+
+    // attention split: a fixed number of pages per work item, so that a row's
+    // result depends only on its own length (batch-invariant logits); the
+    // chunk bound comes from the capacity so one captured graph fits any step
+    const int chunk_pages = kAttnChunkPages;
+    const int max_chunks = (e->max_pages + chunk_pages - 1) / chunk_pages;
+
+    const int d = c.dim, F = c.ffn;
+    for (int l = 0; l < c.layers; l++) {
+        const DeviceLayer &L = e->layers[l];
+        {
+            ProfScope p(e, NDL_PROF_NORM_QUANT);
+            TRY(launch_quantize_rows(e->x, L.attn_norm, rows, d, e->qa, e->sa, s));
+        }
+        {
+            ProfScope p(e, NDL_PROF_GEMM_QKV);
+            TRY(ndl_matmul_i8g32(e->qa, e->sa, rows, L.w_qkv, L.s_qkv, 3 * d, d, e->qkv, 3 * d, nullptr, nullptr, s));
+        }
+        {
+            ProfScope p(e, NDL_PROF_KV_WRITE);
+            KvWriteArgs kw{e->qkv, 3 * d, d_slot, d_pos, e->d_page_table, e->max_pages, e->pool,
+                           (long long)e->page_bytes, e->ec.kv_pages, e->rope_cos, e->rope_sin, l, c.heads, rows,
+                           e->q8, e->qs, e->d_status};
+            TRY(launch_kv_write(kw, s));
+        }
+        {
+            ProfScope p(e, NDL_PROF_ATTENTION);
+            AttnArgs aa{e->q8, e->qs, d_slot, d_pos, d_order, e->d_page_table, e->max_pages, e->pool,
+                        (long long)e->page_bytes, e->ec.kv_pages, l, c.heads, rows, chunk_pages, max_chunks,
+                        1.0f / sqrtf((float)c.head_dim), e->attn, e->partials, e->arrivals, e->d_status};
+            TRY(launch_attn_decode(aa, s));
+        }
+        {
+            ProfScope p(e, NDL_PROF_NORM_QUANT);
+            TRY(launch_quantize_rows(e->attn, nullptr, rows, d, e->qa, e->sa, s));
+        }
+        {
+            ProfScope p(e, NDL_PROF_GEMM_O);
+            TRY(ndl_matmul_i8g32(e->qa, e->sa, rows, L.w_o, L.s_o, d, d, e->x, d, e->x, nullptr, s));
+        }
+        {
+            ProfScope p(e, NDL_PROF_NORM_QUANT);
+            TRY(launch_quantize_rows(e->x, L.ffn_norm, rows, d, e->qa, e->sa, s));
+        }
+        {
+            ProfScope p(e, NDL_PROF_GEMM_GATEUP);
+            TRY(ndl_matmul_i8g32(e->qa, e->sa, rows, L.w_gu, L.s_gu, 2 * F, d, e->gu, 2 * F, nullptr, nullptr, s));
+        }
+        {
+            ProfScope p(e, NDL_PROF_SWIGLU);
+            TRY(launch_swiglu_quantize(e->gu, rows, F, e->act, e->qa, e->sa, s));
+        }
+        {
+            ProfScope p(e, NDL_PROF_GEMM_DOWN);
+            TRY(ndl_matmul_i8g32(e->qa, e->sa, rows, L.w_d, L.s_d, d, F, e->x, d, e->x, nullptr, s));
+        }
+    }
+    if (heads > 0) {
+        ProfScope p(e, NDL_PROF_HEAD);
+        TRY(launch_gather_rows(e->x, d_head, heads, d, e->head_x, s));
+        TRY(launch_quantize_rows(e->head_x, e->final_norm, heads, d, e->qa, e->sa, s));
+        TRY(ndl_matmul_i8g32(e->qa, e->sa, heads, e->w_head, e->s_head, c.vocab, d, e->logits, c.vocab, nullptr,
+                             nullptr, s));
+    }
+    return NDL_OK;
+}
+
+int launch_step_graph(ndl_engine *e, int rows, int heads) {
+    for (auto &g : e->graphs)
+        if (g.rows == rows && g.heads == heads) {
+            g.last_use = ++e->graph_clock;
+            NDL_CUDA(cudaGraphLaunch(g.exec, e->stream));
+            return NDL_OK;
+        }
+    cudaGraph_t graph = nullptr;
+    NDL_CUDA(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal));
+    int st = step_kernels(e, rows, heads);
+    cudaError_t end = cudaStreamEndCapture(e->stream, &graph);
+    if (st != NDL_OK || end != cudaSuccess) {
+        if (graph) cudaGraphDestroy(graph);
+        cudaGetLastError();
+        if (st != NDL_OK) return st;
+        return set_error(NDL_ERR_CUDA, "step capture: %s", cudaGetErrorString(end));
+    }
+    cudaGraphExec_t exec = nullptr;
+    cudaError_t inst = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (inst != cudaSuccess) return set_error(NDL_ERR_CUDA, "step graph: %s", cudaGetErrorString(inst));
+    if (e->graphs.size() >= 16) {  // evict the least recently used shape
+        auto lru = std::min_element(e->graphs.begin(), e->graphs.end(),
+                                    [](const ndl_engine::StepGraph &x, const ndl_engine::StepGraph &y) {
+                                        return x.last_use < y.last_use;
+                                    });
+        cudaGraphExecDestroy(lru->exec);
+        e->graphs.erase(lru);
+    }
+    e->graphs.push_back({rows, heads, exec, ++e->graph_clock});
+    NDL_CUDA(cudaGraphLaunch(exec, e->stream));
+    return NDL_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -390,6 +512,7 @@ NDL_API int ndl_engine_create(const ndl_engine_config *ec, const ndl_decoder_con
 NDL_API int ndl_engine_destroy(ndl_engine *e) {
     if (!e) return NDL_OK;
     if (e->stream) cudaStreamSynchronize(e->stream);
+    for (auto &g : e->graphs) cudaGraphExecDestroy(g.exec);
     for (cudaEvent_t ev : e->event_pool) cudaEventDestroy(ev);
     for (void *p : e->allocations) cudaFree(p);
     if (e->h_meta) cudaFreeHost(e->h_meta);
@@ -561,8 +684,9 @@ NDL_API int ndl_forward_batch(ndl_engine *e, const int *tokens, const int *row_s
         if (head_rows[h] < 0 || head_rows[h] >= rows) return set_error(NDL_ERR_INVALID_ARG, "head row %d", head_rows[h]);
         m[e->off_head + h] = head_rows[h];
     }
-    // pages for the new positions
+    // pages for the new positions; updates region = [count, (slot, index, page)...]
     int n_updates = 0;
+    int32_t *upd = m + e->off_updates;
     for (int r = 0; r < rows; r++) {
         int slot = m[e->off_slot + r], pg = m[e->off_pos + r] / kPagePositions;
         int32_t &entry = e->page_table[(size_t)slot * e->max_pages + pg];
@@ -570,98 +694,32 @@ NDL_API int ndl_forward_batch(ndl_engine *e, const int *tokens, const int *row_s
             if (e->free_pages.empty()) return set_error(NDL_ERR_PAGES_EXHAUSTED, "KV page pool exhausted");
             entry = e->free_pages.back();
             e->free_pages.pop_back();
-            m[e->off_updates + 3 * n_updates] = slot;
-            m[e->off_updates + 3 * n_updates + 1] = pg;
-            m[e->off_updates + 3 * n_updates + 2] = entry;
+            upd[1 + 3 * n_updates] = slot;
+            upd[2 + 3 * n_updates] = pg;
+            upd[3 + 3 * n_updates] = entry;
             n_updates++;
         }
     }
+    upd[0] = n_updates;
     // longest rows first (LPT order for the attention work list)
     std::vector<int> order(rows);
     for (int r = 0; r < rows; r++) order[r] = r;
     std::stable_sort(order.begin(), order.end(),
                      [&](int a, int b) { return m[e->off_pos + a] > m[e->off_pos + b]; });
     for (int r = 0; r < rows; r++) m[e->off_order + r] = order[r];
-    size_t meta_bytes = (size_t)(e->off_updates + 3 * n_updates) * sizeof(int32_t);
-    cudaStream_t s = e->stream;
-    NDL_CUDA(cudaMemcpyAsync(e->d_meta, m, meta_bytes, cudaMemcpyHostToDevice, s));
-    const int32_t *d_tokens = e->d_meta + e->off_tokens, *d_slot = e->d_meta + e->off_slot;
-    const int32_t *d_pos = e->d_meta + e->off_pos, *d_order = e->d_meta + e->off_order;
-    const int32_t *d_head = e->d_meta + e->off_head;
-    {
-        ProfScope p(e, NDL_PROF_PREPARE);
-        TRY(launch_step_prepare(e->d_meta + e->off_updates, n_updates, e->d_page_table, e->max_pages, d_tokens, rows,
-                                e->embedding, c.vocab, c.dim, e->x, e->d_status, s));
-    }
-
-    // attention split: a fixed number of pages per work item, so that a row's
-    // result depends only on its own length (batch-invariant logits)
-    int max_pages_row = 0;
-    for (int r = 0; r < rows; r++) max_pages_row = std::max(max_pages_row, m[e->off_pos + r] / kPagePositions + 1);
-    const int chunk_pages = kAttnChunkPages;
-    const int max_chunks = (max_pages_row + chunk_pages - 1) / chunk_pages;
-
-    const int d = c.dim, F = c.ffn;
-    for (int l = 0; l < c.layers; l++) {
-        const DeviceLayer &L = e->layers[l];
-        {
-            ProfScope p(e, NDL_PROF_NORM_QUANT);
-            TRY(launch_quantize_rows(e->x, L.attn_norm, rows, d, e->qa, e->sa, s));
-        }
-        {
-            ProfScope p(e, NDL_PROF_GEMM_QKV);
-            TRY(ndl_matmul_i8g32(e->qa, e->sa, rows, L.w_qkv, L.s_qkv, 3 * d, d, e->qkv, 3 * d, nullptr, nullptr, s));
-        }
-        {
-            ProfScope p(e, NDL_PROF_KV_WRITE);
-            KvWriteArgs kw{e->qkv, 3 * d, d_slot, d_pos, e->d_page_table, e->max_pages, e->pool,
-                           (long long)e->page_bytes, e->ec.kv_pages, e->rope_cos, e->rope_sin, l, c.heads, rows,
-                           e->q8, e->qs, e->d_status};
-            TRY(launch_kv_write(kw, s));
-        }
-        {
-            ProfScope p(e, NDL_PROF_ATTENTION);
-            AttnArgs aa{e->q8, e->qs, d_slot, d_pos, d_order, e->d_page_table, e->max_pages, e->pool,
-                        (long long)e->page_bytes, e->ec.kv_pages, l, c.heads, rows, chunk_pages, max_chunks,
-                        1.0f / sqrtf((float)c.head_dim), e->attn, e->partials, e->arrivals, e->d_status};
-            TRY(launch_attn_decode(aa, s));
-        }
-        {
-            ProfScope p(e, NDL_PROF_NORM_QUANT);
-            TRY(launch_quantize_rows(e->attn, nullptr, rows, d, e->qa, e->sa, s));
-        }
-        {
-            ProfScope p(e, NDL_PROF_GEMM_O);
-            TRY(ndl_matmul_i8g32(e->qa, e->sa, rows, L.w_o, L.s_o, d, d, e->x, d, e->x, nullptr, s));
-        }
-        {
-            ProfScope p(e, NDL_PROF_NORM_QUANT);
-            TRY(launch_quantize_rows(e->x, L.ffn_norm, rows, d, e->qa, e->sa, s));
-        }
-        {
-            ProfScope p(e, NDL_PROF_GEMM_GATEUP);
-            TRY(ndl_matmul_i8g32(e->qa, e->sa, rows, L.w_gu, L.s_gu, 2 * F, d, e->gu, 2 * F, nullptr, nullptr, s));
-        }
-        {
-            ProfScope p(e, NDL_PROF_SWIGLU);
-            TRY(launch_swiglu_quantize(e->gu, rows, F, e->act, e->qa, e->sa, s));
-        }
-        {
-            ProfScope p(e, NDL_PROF_GEMM_DOWN);
-            TRY(ndl_matmul_i8g32(e->qa, e->sa, rows, L.w_d, L.s_d, d, F, e->x, d, e->x, nullptr, s));
-        }
-    }
-    if (heads > 0) {
-        ProfScope p(e, NDL_PROF_HEAD);
-        TRY(launch_gather_rows(e->x, d_head, heads, d, e->head_x, s));
-        TRY(launch_quantize_rows(e->head_x, e->final_norm, heads, d, e->qa, e->sa, s));
-        TRY(ndl_matmul_i8g32(e->qa, e->sa, heads, e->w_head, e->s_head, c.vocab, d, e->logits, c.vocab, nullptr,
-                             nullptr, s));
-    }
+    size_t meta_bytes = (size_t)(e->off_updates + 1 + 3 * n_updates) * sizeof(int32_t);
+    NDL_CUDA(cudaMemcpyAsync(e->d_meta, m, meta_bytes, cudaMemcpyHostToDevice, e->stream));
+    TRY(e->use_graphs && !e->profile ? launch_step_graph(e, rows, heads) : step_kernels(e, rows, heads));
     // bookkeeping (src/Needle/Engine.cs:2327-2340): lengths advance per slot run
     for (int r = 0; r < rows; r++) e->slot_len[m[e->off_slot + r]] = m[e->off_pos + r] + 1;
     e->last_rows = rows;
     e->last_heads = heads;
+    return NDL_OK;
+}
+
+NDL_API int ndl_engine_use_graphs(ndl_engine *e, int enable) {
+    NDL_REQUIRE(e, "engine is NULL");
+    e->use_graphs = enable != 0;
     return NDL_OK;
 }
 

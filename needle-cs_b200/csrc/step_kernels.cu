@@ -8,16 +8,20 @@
 namespace ndl {
 
 // ---------------------------------------------------------- preparation --
-// Applies (slot, index, page) updates to the device page table, then
-// gathers fp16 embedding rows into the fp32 residual stream x.
-__global__ void __launch_bounds__(256) step_prepare_kernel(const int32_t *__restrict__ updates, int n_updates,
+// Applies (slot, index, page) updates to the device page table (the count
+// is read from device memory so one captured graph serves every step),
+// then gathers fp16 embedding rows into the fp32 residual stream x.
+__global__ void __launch_bounds__(256) step_prepare_kernel(const int32_t *__restrict__ updates,
                                                            int32_t *__restrict__ page_table, int max_pages,
                                                            const int32_t *__restrict__ tokens, int rows,
                                                            const uint16_t *__restrict__ embedding, int vocab,
                                                            int dim, float *__restrict__ x, int *status) {
-    if (blockIdx.x == 0)
+    // updates[0] = count, then (slot, index, page) triples
+    if (blockIdx.x == 0) {
+        const int n_updates = updates[0];
         for (int i = threadIdx.x; i < n_updates; i += blockDim.x)
-            page_table[(size_t)updates[3 * i] * max_pages + updates[3 * i + 1]] = updates[3 * i + 2];
+            page_table[(size_t)updates[1 + 3 * i] * max_pages + updates[2 + 3 * i]] = updates[3 + 3 * i];
+    }
     const int row = blockIdx.x;
     if (row >= rows) return;
     int tok = tokens[row];
@@ -29,12 +33,11 @@ __global__ void __launch_bounds__(256) step_prepare_kernel(const int32_t *__rest
     for (int i = threadIdx.x; i < dim; i += blockDim.x) x[(size_t)row * dim + i] = half_to_float_ref(e[i]);
 }
 
-int launch_step_prepare(const int32_t *updates, int n_updates, int32_t *page_table, int max_pages,
-                        const int32_t *tokens, int rows, const uint16_t *embedding, int vocab, int dim, float *x,
-                        int *status, cudaStream_t stream) {
+int launch_step_prepare(const int32_t *updates, int32_t *page_table, int max_pages, const int32_t *tokens, int rows,
+                        const uint16_t *embedding, int vocab, int dim, float *x, int *status, cudaStream_t stream) {
     int blocks = rows > 0 ? rows : 1;
-    step_prepare_kernel<<<blocks, 256, 0, stream>>>(updates, n_updates, page_table, max_pages, tokens, rows,
-                                                     embedding, vocab, dim, x, status);
+    step_prepare_kernel<<<blocks, 256, 0, stream>>>(updates, page_table, max_pages, tokens, rows, embedding, vocab,
+                                                     dim, x, status);
     return check_launch("step_prepare");
 }
 

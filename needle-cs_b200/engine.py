@@ -152,6 +152,9 @@ class BatchedEngine:
              pr.ctypes.data if with_probs else None)
         return ids, lp, pr
 
+    def use_graphs(self, enable=True):
+        call("ndl_engine_use_graphs", self._h, int(enable))
+
     def profile(self, enable=True):
         call("ndl_engine_profile", self._h, int(enable))
 

@@ -202,3 +202,17 @@ def test_decode_long_sessions_eight_heads(pkg, ops, oracle, cuda):
             ok, err = logits_close(eng.batch_logits_row(s), ref)
             assert ok, f"slot {s}: max err {err}"
             assert ids[s] == int(np.argmax(ref)), f"slot {s}: margin {top2_margin(ref)}"
+
+
+def test_graph_replay_matches_direct_launches(small):
+    """A step replayed from the captured CUDA graph equals direct launches bit for bit."""
+    small.use_graphs(False)
+    _fresh(small)
+    small.forward_batch([5, 77, 9], [0, 2, 3], [0, 1, 2])
+    direct = [small.batch_logits_row(i) for i in range(3)]
+    small.use_graphs(True)
+    for _ in range(2):  # capture, then replay
+        _fresh(small)
+        small.forward_batch([5, 77, 9], [0, 2, 3], [0, 1, 2])
+        for i in range(3):
+            assert np.array_equal(small.batch_logits_row(i), direct[i])
