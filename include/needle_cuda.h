@@ -138,6 +138,30 @@ NDL_API int ndl_matmul_i8g32_batched(const int8_t *q, const float *sa, int m, co
                                      const uint16_t *sw, int n, int k, int batch, long long w_stride,
                                      long long sw_stride, float *y, int ldy, long long y_stride, void *stream);
 
+/* Paged int8 decode attention: the device-pointer counterpart of the
+ * AttentionTile / AttentionBatch kernel slots (Scalar.AttentionHead
+ * src/Needle/Scalar.cs:290-312, AttentionBatch + MergePartials
+ * src/Needle/Blocks.cs:750-990).  For row r and head h it attends to
+ * positions 0..row_pos[r] of slot row_slot[r]:
+ *   s_j = (q . k_j) * ks_j * (qs[r][h] / 8);  p = softmax(s);  out = sum_j p_j vs_j v_j
+ * Page layout: a page holds 64 positions of one slot for every layer; the
+ * (layer, head) record at ((layer*heads + head) * 8704) is
+ *   [K int8 64x64, dims in order k_slot][K scale f32 x64]
+ *   [V^T u8 64x64 = v + 128, positions in order v_slot][V scale f32 x64]
+ * with k_slot(d) = ((d&15)>>2)*16 + (d>>4)*4 + (d&3) and
+ * v_slot(p) = ((p&7)>>1)*16 + (p>>4)*4 + ((p>>3)&1)*2 + (p&1).
+ * q: int8 [rows][heads][64] in k_slot order; qs [rows][heads]; out fp32
+ * [rows][heads][64].  Rows longer than 512 positions are split into
+ * 512-position chunks merged afterwards; the chunk partials live in
+ * `workspace` (NULL: allocated and freed on `stream` by the library).
+ * status (nullable, device int) receives 2 for an out-of-range slot, page
+ * or length and 1 for a timed-out wait; those rows are skipped. */
+NDL_API size_t ndl_attention_paged_workspace(int rows, int heads, int max_pages);
+NDL_API int ndl_attention_paged(const int8_t *q, const float *qs, const int32_t *row_slot, const int32_t *row_pos,
+                                int rows, int heads, const int32_t *page_table, int slots, int max_pages,
+                                const uint8_t *pool, size_t page_bytes, int num_pages, int layer, float *out,
+                                void *workspace, size_t workspace_bytes, int *status, void *stream);
+
 /* ------------------------------------------------------------------ */
 /* Batched decode engine (replaces BatchedEngine + EngineCore slots)   */
 /* ------------------------------------------------------------------ */

@@ -35,6 +35,10 @@ SIGNATURES = {
                                  c_void_p, c_void_p, c_void_p]),
     "ndl_matmul_i8g32_batched": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_int, c_int, c_int, c_ll,
                                          c_ll, c_void_p, c_int, c_ll, c_void_p]),
+    "ndl_attention_paged_workspace": (c_size_t, [c_int, c_int, c_int]),
+    "ndl_attention_paged": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p, c_int, c_int,
+                                    c_void_p, c_size_t, c_int, c_int, c_void_p, c_void_p, c_size_t, c_void_p,
+                                    c_void_p]),
     "ndl_engine_create": (c_int, [c_void_p, c_void_p, ctypes.POINTER(c_void_p)]),
     "ndl_engine_destroy": (c_int, [c_void_p]),
     "ndl_engine_stream": (c_int, [c_void_p, ctypes.POINTER(c_void_p)]),

@@ -130,13 +130,17 @@ __device__ __forceinline__ bool attn_item(const AttnArgs &a, int i, AttnItem &it
     const int ri = rh / a.heads;
     it.row = a.row_order ? a.row_order[ri] : ri;
     it.len = a.row_pos[it.row] + 1;
+    it.slot = a.row_slot[it.row];
+    if (it.len < 1 || it.len > a.max_pages * kPagePositions || it.slot < 0 || it.slot >= a.slots) {
+        if (a.status) atomicOr(a.status, kStatusBadPage);  // out-of-range row: skipped
+        return false;
+    }
     const int pages = (it.len + kPagePositions - 1) / kPagePositions;
     it.n_chunks = (pages + a.chunk_pages - 1) / a.chunk_pages;
     if (chunk >= it.n_chunks) return false;
     it.chunk = chunk;
     it.first_page = chunk * a.chunk_pages;
     it.n_pages = min(pages, it.first_page + a.chunk_pages) - it.first_page;
-    it.slot = a.row_slot[it.row];
     return true;
 }
 
@@ -367,6 +371,7 @@ __global__ void __launch_bounds__(256) attn_merge_kernel(AttnArgs a) {
     if (w >= a.rows * a.heads) return;
     const int row = w / a.heads;
     const int len = a.row_pos[row] + 1;
+    if (len < 1 || len > a.max_pages * kPagePositions) return;
     const int pages = (len + kPagePositions - 1) / kPagePositions;
     const int n_chunks = (pages + a.chunk_pages - 1) / a.chunk_pages;
     if (n_chunks < 2) return;
@@ -413,3 +418,42 @@ int launch_attn_decode(const AttnArgs &a, cudaStream_t stream) {
 }
 
 }  // namespace ndl
+
+using namespace ndl;
+
+static constexpr int kAbiChunkPages = 8;
+
+extern "C" NDL_API size_t ndl_attention_paged_workspace(int rows, int heads, int max_pages) {
+    if (rows <= 0 || heads <= 0 || max_pages <= 0) return 0;
+    const size_t chunks = (size_t)(max_pages + kAbiChunkPages - 1) / kAbiChunkPages;
+    return (size_t)rows * heads * chunks * kPartialFloats * sizeof(float);
+}
+
+extern "C" NDL_API int ndl_attention_paged(const int8_t *q, const float *qs, const int32_t *row_slot,
+                                           const int32_t *row_pos, int rows, int heads, const int32_t *page_table,
+                                           int slots, int max_pages, const uint8_t *pool, size_t page_bytes,
+                                           int num_pages, int layer, float *out, void *workspace,
+                                           size_t workspace_bytes, int *status, void *stream) {
+    NDL_REQUIRE(rows >= 0 && heads >= 1 && slots >= 1 && max_pages >= 1 && num_pages >= 1 && layer >= 0,
+                "bad attention geometry");
+    if (rows == 0) return NDL_OK;
+    NDL_REQUIRE(q && qs && row_slot && row_pos && page_table && pool && out, "null pointer");
+    NDL_REQUIRE(page_bytes % 16 == 0 && page_bytes >= kv_block_offset(layer, heads - 1, heads) + kKvBlockBytes,
+                "page_bytes %zu cannot hold layer %d of %d heads", page_bytes, layer, heads);
+    NDL_REQUIRE(aligned(q, 16) && aligned(pool, 16) && aligned(out, 16) && aligned(qs, 4), "misaligned pointer");
+    const size_t need = ndl_attention_paged_workspace(rows, heads, max_pages);
+    cudaStream_t st = (cudaStream_t)stream;
+    void *ws = workspace;
+    if (ws) {
+        NDL_REQUIRE(workspace_bytes >= need && aligned(ws, 16), "workspace of %zu bytes, %zu needed",
+                    workspace_bytes, need);
+    } else {
+        NDL_CUDA(cudaMallocAsync(&ws, need, st));
+    }
+    AttnArgs a{q, qs, row_slot, row_pos, nullptr, page_table, max_pages, pool, (long long)page_bytes, num_pages,
+               layer, heads, rows, kAbiChunkPages, (max_pages + kAbiChunkPages - 1) / kAbiChunkPages,
+               0.125f, out, static_cast<float *>(ws), nullptr, status, slots};
+    int rc = launch_attn_decode(a, st);
+    if (!workspace) cudaFreeAsync(ws, st);
+    return rc;
+}

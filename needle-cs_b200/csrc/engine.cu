@@ -383,7 +383,8 @@ int step_kernels(ndl_engine *e, int rows, int heads) {
             ProfScope p(e, NDL_PROF_ATTENTION);
             AttnArgs aa{e->q8, e->qs, d_slot, d_pos, d_order, e->d_page_table, e->max_pages, e->pool,
                         (long long)e->page_bytes, e->ec.kv_pages, l, c.heads, rows, chunk_pages, max_chunks,
-                        1.0f / sqrtf((float)c.head_dim), e->attn, e->partials, e->arrivals, e->d_status};
+                        1.0f / sqrtf((float)c.head_dim), e->attn, e->partials, e->arrivals, e->d_status,
+                        e->ec.slots};
             TRY(launch_attn_decode(aa, s));
         }
         {

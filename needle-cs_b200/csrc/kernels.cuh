@@ -64,6 +64,7 @@ struct AttnArgs {
     float *partials;  // [rows][heads][max_chunks][kPartialFloats]
     int *arrivals;    // unused (kept for layout stability)
     int *status;
+    int slots;        // rows of page_table (bounds check)
 };
 int launch_attn_decode(const AttnArgs &a, cudaStream_t stream);
 

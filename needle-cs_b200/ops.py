@@ -91,7 +91,7 @@ def rmsnorm_quantize(x, weight, q=None, scales=None):
 
 
 def matmul_i8g32(q, sa, w, sw, y=None, residual=None, acc=None):
-    """I8G32 linear: y[t][n] = sum_g (half(sw[n][g]) * sa[t]) * D[t][n][g].
+    """I8G32 linear: y[t][n] = sa[t] * (fma chain over groups of half(sw[n][g]) * D[t][n][g]).
 
     q int8 [m,k], sa fp32 [m], w int8 [n,k], sw fp16 bits as int16 [n,k/32].
     """
@@ -114,3 +114,27 @@ def matmul_i8g32_batched(q, sa, w, sw, y):
          _dev(w, torch.int8, "w"), _dev(sw, torch.int16, "sw"), n, k, batch, n * k, n * (k // 32),
          _dev(y, torch.float32, "y"), n, m * n, _stream())
     return y
+
+
+def attention_paged_workspace(rows, heads, max_pages):
+    return lib().ndl_attention_paged_workspace(rows, heads, max_pages)
+
+
+def attention_paged(q8, qs, row_slot, row_pos, page_table, pool, page_bytes, layer, out=None, workspace=None,
+                    status=None):
+    """Paged int8 decode attention (ndl_attention_paged).
+
+    q8 int8 [rows,heads,64] in the page K dim order, qs fp32 [rows,heads],
+    row_slot/row_pos int32 [rows], page_table int32 [slots,max_pages],
+    pool uint8 [num_pages*page_bytes]; out fp32 [rows,heads,64]."""
+    rows, heads, _ = q8.shape
+    slots, max_pages = page_table.shape
+    out = torch.empty((rows, heads, 64), dtype=torch.float32, device=q8.device) if out is None else out
+    ws_ptr, ws_bytes = (None, 0) if workspace is None else (_dev(workspace, torch.uint8, "workspace"),
+                                                             workspace.numel())
+    call("ndl_attention_paged", _dev(q8, torch.int8, "q8"), _dev(qs, torch.float32, "qs"),
+         _dev(row_slot, torch.int32, "row_slot"), _dev(row_pos, torch.int32, "row_pos"), rows, heads,
+         _dev(page_table, torch.int32, "page_table"), slots, max_pages, _dev(pool, torch.uint8, "pool"), page_bytes,
+         pool.numel() // page_bytes, layer, _dev(out, torch.float32, "out"), ws_ptr, ws_bytes,
+         _dev(status, torch.int32, "status") if status is not None else None, _stream())
+    return out

@@ -1,0 +1,74 @@
+"""Builds paged KV pools in the library's page layout from natural-layout
+K/V, for the standalone attention tests."""
+import numpy as np
+
+PAGE_POS = 64
+BLOCK = 8704
+
+
+def k_slot(d):
+    return ((d & 15) >> 2) * 16 + (d >> 4) * 4 + (d & 3)
+
+
+def v_slot(p):
+    return ((p & 7) >> 1) * 16 + (p >> 4) * 4 + ((p >> 3) & 1) * 2 + (p & 1)
+
+
+K_ORDER = np.array([k_slot(d) for d in range(64)])
+V_ORDER = np.array([v_slot(p) for p in range(64)])
+
+
+def make_case(seed, lengths, heads, layers=2, layer=1, max_pages=17):
+    """Random natural-layout K/V/q and the matching paged pool.  Slot s owns
+    pages s*max_pages .. ; returns a dict of numpy arrays."""
+    rng = np.random.default_rng(seed)
+    rows = len(lengths)
+    page_bytes = layers * heads * BLOCK
+    pool = np.zeros(rows * max_pages * page_bytes, np.uint8)
+    cap = max_pages * PAGE_POS
+    K = rng.integers(-128, 128, (rows, cap, heads, 64), dtype=np.int8)
+    V = rng.integers(-128, 128, (rows, cap, heads, 64), dtype=np.int8)
+    KS = rng.uniform(0.0005, 0.004, (rows, cap, heads)).astype(np.float32)
+    VS = rng.uniform(0.001, 0.05, (rows, cap, heads)).astype(np.float32)
+    Q = rng.integers(-128, 128, (rows, heads, 64), dtype=np.int8)
+    QS = rng.uniform(0.2, 0.8, (rows, heads)).astype(np.float32)
+    for s, n in enumerate(lengths):
+        for pg in range((n + 63) // 64):
+            page = s * max_pages + pg
+            lo, hi = pg * 64, min(n, pg * 64 + 64)
+            cnt = hi - lo
+            for h in range(heads):
+                base = page * page_bytes + (layer * heads + h) * BLOCK
+                blk = pool[base:base + BLOCK]
+                kr = np.zeros((64, 64), np.uint8)
+                kr[:cnt][:, K_ORDER] = K[s, lo:hi, h].view(np.uint8)
+                blk[:4096] = kr.reshape(-1)
+                ks = np.zeros(64, np.float32)
+                ks[:cnt] = KS[s, lo:hi, h]
+                blk[4096:4352] = ks.view(np.uint8)
+                vt = np.full((64, 64), 128, np.uint8)
+                vt[:, V_ORDER[:cnt]] = (V[s, lo:hi, h].astype(np.int16) + 128).astype(np.uint8).T
+                blk[4352:8448] = vt.reshape(-1)
+                vs = np.zeros(64, np.float32)
+                vs[:cnt] = VS[s, lo:hi, h]
+                blk[8448:8704] = vs.view(np.uint8)
+    q_perm = np.zeros((rows, heads, 64), np.int8)
+    q_perm[:, :, K_ORDER] = Q
+    page_table = np.array([[s * max_pages + i for i in range(max_pages)] for s in range(rows)], np.int32)
+    return dict(pool=pool, page_bytes=page_bytes, K=K, V=V, KS=KS, VS=VS, Q=Q, QS=QS, q_perm=q_perm,
+                page_table=page_table, row_slot=np.arange(rows, dtype=np.int32),
+                row_pos=np.array([n - 1 for n in lengths], np.int32), heads=heads, layer=layer)
+
+
+def oracle_out(oracle, case, lengths):
+    rows, heads = len(lengths), case["heads"]
+    out = np.zeros((rows, heads, 64), np.float32)
+    for r, n in enumerate(lengths):
+        for h in range(heads):
+            keys = np.ascontiguousarray(case["K"][r, :n, h])
+            vals = np.ascontiguousarray(case["V"][r, :n, h])
+            out[r, h] = oracle.attention_head(case["Q"][r, h], np.float32(case["QS"][r, h]), keys,
+                                              np.ascontiguousarray(case["KS"][r, :n, h]), vals,
+                                              np.ascontiguousarray(case["VS"][r, :n, h]), 64, 64, 1, 0, n - 1, 64,
+                                              64, np.float32(0.125))
+    return out
