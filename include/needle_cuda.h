@@ -162,6 +162,23 @@ NDL_API int ndl_attention_paged(const int8_t *q, const float *qs, const int32_t 
                                 const uint8_t *pool, size_t page_bytes, int num_pages, int layer, float *out,
                                 void *workspace, size_t workspace_bytes, int *status, void *stream);
 
+/* ndl_attention_paged for callers that cannot allocate.  No counterpart in
+ * the reference: it exists for hosts that must not allocate while serving
+ * (frame-budgeted game or job threads, audio callbacks, zero-allocation
+ * request loops), where cudaMalloc could block or synchronise the device.
+ * Same arguments and results as ndl_attention_paged, without a workspace:
+ * the chunk partials live in a 4 MiB device array owned by the library
+ * (held on every GPU that loads it until exit).  Requests whose workspace
+ * (ndl_attention_paged_workspace) exceeds 4 MiB are rejected with
+ * NDL_ERR_INVALID_ARG.  The first call on a device looks the array up
+ * (cudaGetSymbolAddress) and must come before any stream capture.  All
+ * calls share the array: calls that overlap on the GPU race and must be
+ * ordered by the caller (e.g. one stream).  Allocates nothing. */
+NDL_API int ndl_attention_paged_noalloc(const int8_t *q, const float *qs, const int32_t *row_slot,
+                                        const int32_t *row_pos, int rows, int heads, const int32_t *page_table,
+                                        int slots, int max_pages, const uint8_t *pool, size_t page_bytes,
+                                        int num_pages, int layer, float *out, int *status, void *stream);
+
 /* ------------------------------------------------------------------ */
 /* Batched decode engine (replaces BatchedEngine + EngineCore slots)   */
 /* ------------------------------------------------------------------ */

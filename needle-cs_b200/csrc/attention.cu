@@ -17,6 +17,8 @@
 // on the row's own length) writes (peak, sum, unnormalised output) partials
 // that attn_merge_kernel combines with exp(peak - max) weights, like
 // MergePartials.
+#include <mutex>
+
 #include "common.cuh"
 #include "kernels.cuh"
 #include "kv.cuh"
@@ -456,4 +458,85 @@ extern "C" NDL_API int ndl_attention_paged(const int8_t *q, const float *qs, con
     int rc = launch_attn_decode(a, st);
     if (!workspace) cudaFreeAsync(ws, st);
     return rc;
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of ndl_attention_paged.
+//
+// Some hosts must not allocate memory while they serve a request: a game
+// loop or job-system worker on a frame budget, an audio callback, or the
+// reference's host worker, whose steady-state calls are held to zero
+// allocations.  cudaMalloc can block for a long time, serialises on a
+// driver-wide lock and can synchronise the device, so such callers cannot
+// supply the workspace ndl_attention_paged needs, nor let it allocate one.
+// This entry point keeps the chunk partials in a fixed device array that
+// the library owns instead.
+//
+// The array is a file-scope __device__ variable, so every GPU that loads
+// this library holds its kNoAllocScratchBytes until the process exits.  On
+// the host its name is only a stand-in: the real device address is looked
+// up once per device with cudaGetSymbolAddress, the first time the entry
+// point is called on that device (with that device current), and cached.
+// Make that first call before any stream capture starts.
+//
+// Every call shares the one array.  Nothing in it has to start at zero: a
+// launch writes each chunk partial before the merge reads it.  Two calls
+// whose work overlaps on the GPU (different streams, or no ordering between
+// them) race on the array and can corrupt each other's results; callers
+// must order them, for example by issuing them on one stream.
+// ---------------------------------------------------------------------------
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = 4u << 20;  // 4 MiB: 512 rows x 8 heads x 3 chunks fits
+constexpr int kNoAllocMaxDevices = 64;
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+std::mutex g_noalloc_mutex;
+void *g_noalloc_address[kNoAllocMaxDevices];
+
+// Device address of the scratch array on the current device (set-up on
+// first use per device).
+int noalloc_scratch(void **out) {
+    int dev = 0;
+    NDL_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= kNoAllocMaxDevices) return set_error(NDL_ERR_UNSUPPORTED, "device %d out of range", dev);
+    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+    if (!g_noalloc_address[dev]) {
+        void *ptr = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+        if (e != cudaSuccess || !ptr)
+            return set_error(NDL_ERR_CUDA, "cudaGetSymbolAddress(scratch): %s", cudaGetErrorString(e));
+        g_noalloc_address[dev] = ptr;
+    }
+    *out = g_noalloc_address[dev];
+    return NDL_OK;
+}
+
+}  // namespace
+
+extern "C" NDL_API int ndl_attention_paged_noalloc(const int8_t *q, const float *qs, const int32_t *row_slot,
+                                                   const int32_t *row_pos, int rows, int heads,
+                                                   const int32_t *page_table, int slots, int max_pages,
+                                                   const uint8_t *pool, size_t page_bytes, int num_pages, int layer,
+                                                   float *out, int *status, void *stream) {
+    NDL_REQUIRE(rows >= 0 && heads >= 1 && slots >= 1 && max_pages >= 1 && num_pages >= 1 && layer >= 0,
+                "bad attention geometry");
+    if (rows == 0) return NDL_OK;
+    NDL_REQUIRE(q && qs && row_slot && row_pos && page_table && pool && out, "null pointer");
+    NDL_REQUIRE(page_bytes % 16 == 0 && page_bytes >= kv_block_offset(layer, heads - 1, heads) + kKvBlockBytes,
+                "page_bytes %zu cannot hold layer %d of %d heads", page_bytes, layer, heads);
+    NDL_REQUIRE(aligned(q, 16) && aligned(pool, 16) && aligned(out, 16) && aligned(qs, 4), "misaligned pointer");
+    const size_t need = ndl_attention_paged_workspace(rows, heads, max_pages);
+    if (need > kNoAllocScratchBytes)
+        return set_error(NDL_ERR_INVALID_ARG,
+                         "%d rows x %d heads x %d pages need %zu bytes of scratch; the built-in buffer holds %zu",
+                         rows, heads, max_pages, need, kNoAllocScratchBytes);
+    void *scratch = nullptr;
+    int st = noalloc_scratch(&scratch);
+    if (st != NDL_OK) return st;
+    AttnArgs a{q, qs, row_slot, row_pos, nullptr, page_table, max_pages, pool, (long long)page_bytes, num_pages,
+               layer, heads, rows, kAbiChunkPages, (max_pages + kAbiChunkPages - 1) / kAbiChunkPages,
+               0.125f, out, static_cast<float *>(scratch), nullptr, status, slots};
+    return launch_attn_decode(a, (cudaStream_t)stream);
 }
