@@ -9,7 +9,7 @@
 // AttentionBatch.ExecuteChunk + MergePartials src/Needle/Blocks.cs:750-990):
 // persistent warps stream (row, head, chunk of pages) items.  Each page's
 // 8704-byte (layer, head) record arrives in shared memory by one
-// cp.async.bulk (3-stage ring, mbarrier completion, bounded waits).  Scores
+// cp.async.bulk (2-stage ring per warp, mbarrier completion, bounded waits).  Scores
 // are exact int8 dots (mma.sync s8) scaled by ks * (qs / sqrt(d)); softmax
 // is online (running max, rescaled sum) in fp32 with expf; V is accumulated
 // in fp32 by mma.sync f16 with hi/lo-split probability weights.  A row
@@ -115,7 +115,7 @@ int launch_kv_write(const KvWriteArgs &a, cudaStream_t stream) {
 
 // ------------------------------------------------------ decode attention --
 constexpr int kAttnWarps = 4;
-constexpr int kAttnStages = 3;
+constexpr int kAttnStages = 2;
 constexpr int kWarpSmem = kAttnStages * kKvBlockBytes + 64;  // ring + barriers
 constexpr uint32_t kWaitLimit = 1u << 22;
 
@@ -174,7 +174,7 @@ __device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
 }
 
 // Persistent: each warp walks items warp_gid, warp_gid + W, ... and streams
-// their pages through its 3-stage ring without draining between items.
+// their pages through its 2-stage ring without draining between items.
 // Per page (64 positions):
 //  * QK: mma.sync m16n8k32 s8, A = the query in every row, B = K (k = dims,
 //    n = positions): exact int32 dots; lane L ends up owning positions 2L and
@@ -183,7 +183,7 @@ __device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
 //    fp16(w' - row 0) with w' = p * vs * 2^e (hi/lo split, ~22-bit
 //    weights), B = V (exact in fp16).  e keeps w' below 2^12 and is folded
 //    into the online-softmax rescale.
-__global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(AttnArgs a) {
+__global__ void __launch_bounds__(kAttnWarps * 32, 3) attn_decode_kernel(AttnArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int gid = lane >> 2, tig = lane & 3;
@@ -273,20 +273,28 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(AttnArgs a
             }
             const int p0 = 2 * lane, p1 = p0 + 1;
             const float2 ks = *reinterpret_cast<const float2 *>(blk + kKScaleOffset + 8 * lane);
+            const float2 vs = *reinterpret_cast<const float2 *>(blk + kVScaleOffset + 8 * lane);
             const float s0 = p0 < valid ? __fmul_rn(__fmul_rn(__int2float_rn(dot0), ks.x), scale) : -INFINITY;
             const float s1 = p1 < valid ? __fmul_rn(__fmul_rn(__int2float_rn(dot1), ks.y), scale) : -INFINITY;
-            const float m_new = fmaxf(m, warp_max_f(fmaxf(s0, s1)));
+            // one combined warp reduction: the page's score max and V-scale max
+            float smax = fmaxf(s0, s1);
+            float vmax = fmaxf(p0 < valid ? vs.x : 0.0f, p1 < valid ? vs.y : 0.0f);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                smax = fmaxf(smax, __shfl_xor_sync(0xffffffffu, smax, o));
+                vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, o));
+            }
+            const float m_new = fmaxf(m, smax);
             const float e0 = p0 < valid ? expf(s0 - m_new) : 0.0f;
             const float e1 = p1 < valid ? expf(s1 - m_new) : 0.0f;
             const float corr = expf(m - m_new);
-            l = l * corr + warp_sum_f(e0 + e1);
+            l = l * corr + (e0 + e1);  // this lane's share; reduced across the warp per item
             m = m_new;
-            const float2 vs = *reinterpret_cast<const float2 *>(blk + kVScaleOffset + 8 * lane);
             const float w0 = p0 < valid ? e0 * vs.x : 0.0f;
             const float w1 = p1 < valid ? e1 * vs.y : 0.0f;
-            // power-of-two range guard: w' = w * 2^e < 2^12
+            // power-of-two range guard: w' = w * 2^e < 2^12 (w <= vs since p <= 1)
             int ex;
-            frexpf(warp_max_f(fmaxf(w0, w1)), &ex);
+            frexpf(vmax, &ex);
             const int e_page = 12 - max(0, ex);
             const float rescale = corr * exp2f((float)(e_page - e_acc));
             e_acc = e_page;
@@ -295,10 +303,12 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(AttnArgs a
             const float h0 = __half2float(__float2half_rn(x0)), h1 = __half2float(__float2half_rn(x1));
             const uint32_t H = pack_h2(h0, h1);
             const uint32_t Lo = pack_h2(x0 - h0, x1 - h1);
+            if (rescale != 1.0f) {
 #pragma unroll
-            for (int nt = 0; nt < 8; nt++)
+                for (int nt = 0; nt < 8; nt++)
 #pragma unroll
-                for (int i = 0; i < 4; i++) acc[nt][i] *= rescale;
+                    for (int i = 0; i < 4; i++) acc[nt][i] *= rescale;
+            }
             // ---- PV ----
             uint32_t A0[4], A2[4];  // row gid (0 = hi, 1 = lo) of the four k-steps
 #pragma unroll
@@ -324,6 +334,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(AttnArgs a
             if (lane == 0 && advance_producer()) issue_one();
         }
         if (timed_out) break;
+        l = warp_sum_f(l);
         // rows 0 (hi) and 1 (lo) live in lanes 0-3 and 4-7: o = (hi + lo) * 2^-e
         const float unscale = exp2f((float)(-e_acc));
         float o[8][2];
@@ -409,7 +420,7 @@ int launch_attn_decode(const AttnArgs &a, cudaStream_t stream) {
     const long long items = (long long)a.rows * a.heads * a.max_chunks;
     if (items > 0x7FFFFFFF) return set_error(NDL_ERR_INVALID_ARG, "attention: too many work items");
     long long blocks = (items + kAttnWarps - 1) / kAttnWarps;
-    const long long resident = (long long)sms * 2;  // two CTAs per SM fit the shared memory
+    const long long resident = (long long)sms * 3;  // three CTAs (12 warps) per SM fit the shared memory
     if (blocks > resident) blocks = resident;
     attn_decode_kernel<<<(unsigned)blocks, kAttnWarps * 32, smem, stream>>>(a);
     int st = check_launch("attn_decode");
