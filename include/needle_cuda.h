@@ -146,10 +146,14 @@ NDL_API int ndl_matmul_i8g32_batched(const int8_t *q, const float *sa, int m, co
  *   s_j = (q . k_j) * ks_j * (qs[r][h] / 8);  p = softmax(s);  out = sum_j p_j vs_j v_j
  * Page layout: a page holds 64 positions of one slot for every layer; the
  * (layer, head) record at ((layer*heads + head) * 8704) is
- *   [K int8 64x64, dims in order k_slot][K scale f32 x64]
- *   [V^T u8 64x64 = v + 128, positions in order v_slot][V scale f32 x64]
- * with k_slot(d) = ((d&15)>>2)*16 + (d>>4)*4 + (d&3) and
- * v_slot(p) = ((p&7)>>1)*16 + (p>>4)*4 + ((p>>3)&1)*2 + (p&1).
+ *   [K int8 64x64][K scale f32 x64][V^T int8 64x64][V scale f32 x64]
+ * K (row = position p, col = dim d) and V^T (row = d, col = pv_col(p)) are
+ * stored in mma m16n8k32 A-fragment order: element (row, col) at byte
+ *   (row>>4)*1024 + (col>>5)*512 + ((row&7)*4 + (col>>2&3))*16
+ *   + ((row>>3&1) + 2*(col>>4&1))*4 + (col&3)
+ * with pv_col(p) = 32*(g>>2) + 16*(g>>1&1) + 4*(p>>4&3) + 2*(g&1) + (p>>3&1),
+ * g = p&7; the scales of p sit at index 2*((p&7)*4 + (p>>4&3)) + (p>>3&1).
+ * The query's dims are in the order k_slot(d) = ((d&15)>>2)*16 + (d>>4)*4 + (d&3).
  * q: int8 [rows][heads][64] in k_slot order; qs [rows][heads]; out fp32
  * [rows][heads][64].  Rows longer than 512 positions are split into
  * 512-position chunks merged afterwards; the chunk partials live in

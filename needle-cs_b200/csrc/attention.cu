@@ -89,9 +89,9 @@ __global__ void __launch_bounds__(256) kv_write_kernel(KvWriteArgs a) {
         float hi = __fadd_rn(__fmul_rn(x1, c), __fmul_rn(x0, s));
         float scale = warp_quantize64(lo, hi, lo8, hi8);
         if (ok) {
-            blk[j * kHeadDim + k_slot(lane)] = (uint8_t)lo8;
-            blk[j * kHeadDim + k_slot(lane + 32)] = (uint8_t)hi8;
-            if (lane == 0) reinterpret_cast<float *>(blk + kKScaleOffset)[j] = scale;
+            blk[k_byte(j, lane)] = (uint8_t)lo8;
+            blk[k_byte(j, lane + 32)] = (uint8_t)hi8;
+            if (lane == 0) reinterpret_cast<float *>(blk + kKScaleOffset)[scale_slot(j)] = scale;
         }
     }
     // v: per-(position, head) quantize into the page
@@ -99,9 +99,9 @@ __global__ void __launch_bounds__(256) kv_write_kernel(KvWriteArgs a) {
         const float *vb = base + 2 * width;
         float scale = warp_quantize64(vb[lane], vb[lane + 32], lo8, hi8);
         if (ok) {
-            blk[kVOffset + lane * kHeadDim + v_slot(j)] = (uint8_t)(lo8 + 128);
-            blk[kVOffset + (lane + 32) * kHeadDim + v_slot(j)] = (uint8_t)(hi8 + 128);
-            if (lane == 0) reinterpret_cast<float *>(blk + kVScaleOffset)[j] = scale;
+            blk[v_byte(j, lane)] = (uint8_t)lo8;
+            blk[v_byte(j, lane + 32)] = (uint8_t)hi8;
+            if (lane == 0) reinterpret_cast<float *>(blk + kVScaleOffset)[scale_slot(j)] = scale;
         }
     }
 }
@@ -116,7 +116,11 @@ int launch_kv_write(const KvWriteArgs &a, cudaStream_t stream) {
 // ------------------------------------------------------ decode attention --
 constexpr int kAttnWarps = 4;
 constexpr int kAttnStages = 2;
-constexpr int kWarpSmem = kAttnStages * kKvBlockBytes + 64;  // ring + barriers
+constexpr int kDigitOffset = kAttnStages * kKvBlockBytes + 64;  // after the ring and its barriers
+constexpr int kWarpSmem = kDigitOffset + 256;                     // + PV weight digits [4][64]
+// int32 PV accumulators gain at most 64 * 255 * 128 per page; flushing to
+// fp32 every 1024 pages keeps them below 2^31.
+constexpr int kHoldPages = 1024;
 constexpr uint32_t kWaitLimit = 1u << 22;
 
 
@@ -146,43 +150,34 @@ __device__ __forceinline__ bool attn_item(const AttnArgs &a, int i, AttnItem &it
     return true;
 }
 
-__device__ __forceinline__ void mma_s8_m16n8k32(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                                uint32_t b0, uint32_t b1) {
+__device__ __forceinline__ void mma_s8s8_m16n8k32(int (&d)[4], const uint4 &a, uint32_t b0, uint32_t b1) {
     asm volatile(
         "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
         "{%0,%1,%2,%3};\n"
         : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+        : "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w), "r"(b0), "r"(b1));
 }
-__device__ __forceinline__ void mma_f16_m16n8k16(float (&d)[4], uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
+__device__ __forceinline__ void mma_s8u8_m16n8k32(int (&d)[4], const uint4 &a, uint32_t b0, uint32_t b1) {
     asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
         "{%0,%1,%2,%3};\n"
-        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
-}
-// Two biased bytes (v + 128) -> exact fp16 pair: splice under the exponent of
-// 1024 and subtract 1152.
-__device__ __forceinline__ uint32_t u8x2_to_h2(uint32_t word, uint32_t selector) {
-    uint32_t h = __byte_perm(word, 0x64646464u, selector);
-    __half2 r = __hsub2(*reinterpret_cast<__half2 *>(&h), __floats2half2_rn(1152.0f, 1152.0f));
-    return *reinterpret_cast<uint32_t *>(&r);
-}
-__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
-    __half2 r = __floats2half2_rn(lo, hi);
-    return *reinterpret_cast<uint32_t *>(&r);
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w), "r"(b0), "r"(b1));
 }
 
 // Persistent: each warp walks items warp_gid, warp_gid + W, ... and streams
 // their pages through its 2-stage ring without draining between items.
-// Per page (64 positions):
-//  * QK: mma.sync m16n8k32 s8, A = the query in every row, B = K (k = dims,
-//    n = positions): exact int32 dots; lane L ends up owning positions 2L and
-//    2L+1 for the softmax.
-//  * PV: mma.sync m16n8k16 f16 -> f32, A row 0 = fp16(w'), row 1 =
-//    fp16(w' - row 0) with w' = p * vs * 2^e (hi/lo split, ~22-bit
-//    weights), B = V (exact in fp16).  e keeps w' below 2^12 and is folded
-//    into the online-softmax rescale.
+// Per page (64 positions), all products on int8 tensor cores:
+//  * QK: mma.sync m16n8k32 s8, A = K (16 positions x 32 dims), B = the
+//    query in every column: exact int32 dots.  Lane (gid, tig) keeps tile
+//    tig, i.e. positions 16*tig + gid and 16*tig + gid + 8.
+//  * PV: the weights w' = p * vs * 2^e (e keeps w' below 2^12, folded into
+//    the online-softmax rescale) become 24-bit fixed point W = w' * 2^12,
+//    split into three unsigned byte digits.  mma.sync m16n8k32 s8 x u8 with
+//    A = V^T (16 dims x 32 positions) and B = the digits (column = digit)
+//    gives exact int32 sums of digit x v, chained across pages in the
+//    accumulator until the softmax rescale changes; the digits recombine
+//    as D0 * 2^16 + D1 * 2^8 + D2 once per item.
 __global__ void __launch_bounds__(kAttnWarps * 32, 3) attn_decode_kernel(AttnArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -192,10 +187,12 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 3) attn_decode_kernel(AttnArg
 
     uint8_t *ring = smem + warp * kWarpSmem;
     uint64_t *bars = reinterpret_cast<uint64_t *>(ring + kAttnStages * kKvBlockBytes);
+    uint8_t *digits = ring + kDigitOffset;  // [digit 0..2, unused zero row][tig][16 bytes]
     if (lane == 0) {
         for (int s = 0; s < kAttnStages; s++) mbar_init(&bars[s], 1);
         fence_mbar_init();
     }
+    reinterpret_cast<uint2 *>(digits)[lane] = make_uint2(0u, 0u);
     __syncwarp();
 
     // Items are dealt in a snake order over rows sorted longest first: round
@@ -250,9 +247,14 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 3) attn_decode_kernel(AttnArg
         const float scale = __fmul_rn(a.qs[(size_t)it.row * a.heads + it.head], a.inv_sqrt_d);
         float m = -INFINITY, l = 0.0f;
         int e_acc = 12;  // power-of-two scale currently applied to the accumulators
-        float acc[8][4];
+        int acc_i[4][4];
+        float acc_f[4][4];
 #pragma unroll
-        for (int nt = 0; nt < 8; nt++) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.0f;
+        for (int mt = 0; mt < 4; mt++)
+#pragma unroll
+            for (int i = 0; i < 4; i++) acc_i[mt][i] = 0, acc_f[mt][i] = 0.0f;
+        int held = 0;  // pages summed in acc_i since the last flush
+        const int p0 = 16 * tig + gid, p1 = p0 + 8;
         for (int pg = 0; pg < it.n_pages; pg++) {
             const int stage = consumed % kAttnStages;
             if (!mbar_wait_bounded(&bars[stage], (consumed / kAttnStages) & 1, kWaitLimit)) {
@@ -261,17 +263,17 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 3) attn_decode_kernel(AttnArg
             }
             const uint8_t *blk = ring + stage * kKvBlockBytes;
             const int valid = min(kPagePositions, it.len - (it.first_page + pg) * kPagePositions);
-            // ---- QK: dots for positions nt*8 + 2*tig + {0,1}, every n-tile ----
+            // ---- QK ----
             int dot0 = 0, dot1 = 0;
 #pragma unroll
-            for (int nt = 0; nt < 8; nt++) {
-                const uint4 kc = *reinterpret_cast<const uint4 *>(blk + (nt * 8 + gid) * kHeadDim + tig * 16);
+            for (int mt = 0; mt < 4; mt++) {
+                const uint4 k0 = *reinterpret_cast<const uint4 *>(blk + mt * 1024 + lane * 16);
+                const uint4 k1 = *reinterpret_cast<const uint4 *>(blk + mt * 1024 + 512 + lane * 16);
                 int d[4] = {0, 0, 0, 0};
-                mma_s8_m16n8k32(d, qv.x, qv.x, qv.y, qv.y, kc.x, kc.y);
-                mma_s8_m16n8k32(d, qv.z, qv.z, qv.w, qv.w, kc.z, kc.w);
-                if (nt == gid) dot0 = d[0], dot1 = d[1];  // lane L keeps positions 2L, 2L+1
+                mma_s8s8_m16n8k32(d, k0, qv.x, qv.y);
+                mma_s8s8_m16n8k32(d, k1, qv.z, qv.w);
+                if (mt == tig) dot0 = d[0], dot1 = d[2];
             }
-            const int p0 = 2 * lane, p1 = p0 + 1;
             const float2 ks = *reinterpret_cast<const float2 *>(blk + kKScaleOffset + 8 * lane);
             const float2 vs = *reinterpret_cast<const float2 *>(blk + kVScaleOffset + 8 * lane);
             const float s0 = p0 < valid ? __fmul_rn(__fmul_rn(__int2float_rn(dot0), ks.x), scale) : -INFINITY;
@@ -290,44 +292,42 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 3) attn_decode_kernel(AttnArg
             const float corr = expf(m - m_new);
             l = l * corr + (e0 + e1);  // this lane's share; reduced across the warp per item
             m = m_new;
-            const float w0 = p0 < valid ? e0 * vs.x : 0.0f;
-            const float w1 = p1 < valid ? e1 * vs.y : 0.0f;
-            // power-of-two range guard: w' = w * 2^e < 2^12 (w <= vs since p <= 1)
+            // power-of-two range guard: w' = p * vs * 2^e < 2^12 (p <= 1)
             int ex;
             frexpf(vmax, &ex);
             const int e_page = 12 - max(0, ex);
             const float rescale = corr * exp2f((float)(e_page - e_acc));
             e_acc = e_page;
-            const float f = exp2f((float)e_page);
-            const float x0 = w0 * f, x1 = w1 * f;
-            const float h0 = __half2float(__float2half_rn(x0)), h1 = __half2float(__float2half_rn(x1));
-            const uint32_t H = pack_h2(h0, h1);
-            const uint32_t Lo = pack_h2(x0 - h0, x1 - h1);
-            if (rescale != 1.0f) {
+            const float f = exp2f((float)(e_page + 12));
+            // W = w' * 2^12 < 2^24 (an exact power-of-two scaling of w')
+            const uint32_t W0 = p0 < valid ? __float2uint_rn(e0 * vs.x * f) : 0u;
+            const uint32_t W1 = p1 < valid ? __float2uint_rn(e1 * vs.y * f) : 0u;
+            // digits of this lane's two positions, at PV columns pv_col(p0) and pv_col(p0) + 1
+            uint8_t *dg = digits + tig * 16 + 2 * gid;
+            *reinterpret_cast<uint16_t *>(dg) = (uint16_t)__byte_perm(W0, W1, 0x0062);
+            *reinterpret_cast<uint16_t *>(dg + 64) = (uint16_t)__byte_perm(W0, W1, 0x0051);
+            *reinterpret_cast<uint16_t *>(dg + 128) = (uint16_t)__byte_perm(W0, W1, 0x0040);
+            if (rescale != 1.0f || held == kHoldPages) {
 #pragma unroll
-                for (int nt = 0; nt < 8; nt++)
+                for (int mt = 0; mt < 4; mt++)
 #pragma unroll
-                    for (int i = 0; i < 4; i++) acc[nt][i] *= rescale;
+                    for (int i = 0; i < 4; i++) {
+                        acc_f[mt][i] = (acc_f[mt][i] + __int2float_rn(acc_i[mt][i])) * rescale;
+                        acc_i[mt][i] = 0;
+                    }
+                held = 0;
             }
-            // ---- PV ----
-            uint32_t A0[4], A2[4];  // row gid (0 = hi, 1 = lo) of the four k-steps
-#pragma unroll
-            for (int ks_ = 0; ks_ < 4; ks_++) {
-                const uint32_t ha = __shfl_sync(0xffffffffu, H, 8 * ks_ + tig);
-                const uint32_t la = __shfl_sync(0xffffffffu, Lo, 8 * ks_ + tig);
-                const uint32_t hb = __shfl_sync(0xffffffffu, H, 8 * ks_ + 4 + tig);
-                const uint32_t lb = __shfl_sync(0xffffffffu, Lo, 8 * ks_ + 4 + tig);
-                A0[ks_] = gid == 0 ? ha : (gid == 1 ? la : 0u);
-                A2[ks_] = gid == 0 ? hb : (gid == 1 ? lb : 0u);
-            }
+            held++;
+            __syncwarp();
+            // ---- PV: column n of B is digit n & 3 (digit 3 = the zero row) ----
+            const uint4 b = *reinterpret_cast<const uint4 *>(digits + (gid & 3) * 64 + tig * 16);
             const uint8_t *vt = blk + kVOffset;
 #pragma unroll
-            for (int nt = 0; nt < 8; nt++) {
-                const uint4 vc = *reinterpret_cast<const uint4 *>(vt + (nt * 8 + gid) * kHeadDim + tig * 16);
-                const uint32_t vw[4] = {vc.x, vc.y, vc.z, vc.w};
-#pragma unroll
-                for (int ks_ = 0; ks_ < 4; ks_++)
-                    mma_f16_m16n8k16(acc[nt], A0[ks_], A2[ks_], u8x2_to_h2(vw[ks_], 0x4140), u8x2_to_h2(vw[ks_], 0x4342));
+            for (int mt = 0; mt < 4; mt++) {
+                const uint4 v0 = *reinterpret_cast<const uint4 *>(vt + mt * 1024 + lane * 16);
+                const uint4 v1 = *reinterpret_cast<const uint4 *>(vt + mt * 1024 + 512 + lane * 16);
+                mma_s8u8_m16n8k32(acc_i[mt], v0, b.x, b.y);
+                mma_s8u8_m16n8k32(acc_i[mt], v1, b.z, b.w);
             }
             __syncwarp();
             consumed++;
@@ -335,33 +335,41 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 3) attn_decode_kernel(AttnArg
         }
         if (timed_out) break;
         l = warp_sum_f(l);
-        // rows 0 (hi) and 1 (lo) live in lanes 0-3 and 4-7: o = (hi + lo) * 2^-e
-        const float unscale = exp2f((float)(-e_acc));
-        float o[8][2];
+        // lane (gid, 0) holds digits 0 and 1 of dims 16*mt + gid (+8), lane
+        // (gid, 1) digit 2: o = (D0 * 2^16 + D1 * 2^8 + D2) * 2^-(12 + e)
+        const float unscale = exp2f((float)(-12 - e_acc));
+        float o[4][2];
 #pragma unroll
-        for (int nt = 0; nt < 8; nt++) {
-            const float lo0 = __shfl_down_sync(0xffffffffu, acc[nt][0], 4);
-            const float lo1 = __shfl_down_sync(0xffffffffu, acc[nt][1], 4);
-            o[nt][0] = (acc[nt][0] + lo0) * unscale;
-            o[nt][1] = (acc[nt][1] + lo1) * unscale;
+        for (int mt = 0; mt < 4; mt++) {
+            float t[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++) t[i] = acc_f[mt][i] + __int2float_rn(acc_i[mt][i]);
+            const float d2a = __shfl_down_sync(0xffffffffu, t[0], 1);
+            const float d2b = __shfl_down_sync(0xffffffffu, t[2], 1);
+            o[mt][0] = fmaf(t[0], 65536.0f, fmaf(t[1], 256.0f, d2a)) * unscale;
+            o[mt][1] = fmaf(t[2], 65536.0f, fmaf(t[3], 256.0f, d2b)) * unscale;
         }
         const size_t rh_index = (size_t)it.row * a.heads + it.head;
         float *out = a.out + rh_index * kHeadDim;
         if (it.n_chunks == 1) {
             const float inv = 1.0f / l;
-            if (lane < 4)
+            if (tig == 0)
 #pragma unroll
-                for (int nt = 0; nt < 8; nt++)
-                    *reinterpret_cast<float2 *>(out + nt * 8 + 2 * tig) = make_float2(o[nt][0] * inv, o[nt][1] * inv);
+                for (int mt = 0; mt < 4; mt++) {
+                    out[16 * mt + gid] = o[mt][0] * inv;
+                    out[16 * mt + gid + 8] = o[mt][1] * inv;
+                }
             continue;
         }
         // long row: publish this chunk's (unnormalised output, peak, sum);
         // attn_merge_kernel combines them after this launch
         float *part = a.partials + (rh_index * a.max_chunks + it.chunk) * kPartialFloats;
-        if (lane < 4)
+        if (tig == 0)
 #pragma unroll
-            for (int nt = 0; nt < 8; nt++)
-                *reinterpret_cast<float2 *>(part + nt * 8 + 2 * tig) = make_float2(o[nt][0], o[nt][1]);
+            for (int mt = 0; mt < 4; mt++) {
+                part[16 * mt + gid] = o[mt][0];
+                part[16 * mt + gid + 8] = o[mt][1];
+            }
         if (lane == 0) {
             part[64] = m;
             part[65] = l;

@@ -2,18 +2,20 @@
 //
 // A page holds 64 consecutive positions of one slot for every layer.  Inside
 // a page, the block of (layer, head) is one contiguous 8704-byte record
-//     [K int8 64x64][K scale f32 x64][V^T u8 64x64][V scale f32 x64]
+//     [K int8 64x64][K scale f32 x64][V^T int8 64x64][V scale f32 x64]
 // so a single 16-byte-aligned bulk copy brings everything attention needs
 // for 64 positions of one head into shared memory.  This replaces the
 // reference's flat per-slot arrays [layer][capacity][kvWidth] + scales
 // (src/Needle/Engine.cs:184-187,220-223) with the same per-(position, head)
 // int8 + fp32-scale contents, rearranged for the tensor-core fragments:
-//  * K row j (position j) at 64*j, its 64 dims in the order k_slot(d), so a
-//    lane's m16n8k32 B fragments for both k-steps are one 16-byte chunk;
-//  * V transposed, row d at kVOffset + 64*d, positions in the order
-//    v_slot(p) so a lane's m16n8k16 B fragments for all four k-steps are one
-//    16-byte chunk; bytes hold v + 128 (unsigned) for a 2-op fp16 convert.
-// The query vector uses the K dim order too.
+//  * K (row = position, col = dim) and V^T (row = dim, col = pv_col of the
+//    position) are int8 64x64 matrices stored in m16n8k32 A-fragment order
+//    (frag_byte): a lane's four A registers of one (16-row tile, 32-col
+//    k-step) are one 16-byte chunk and a warp reads 512 contiguous bytes;
+//  * the scales of position p sit at scale_slot(p), so the lane that owns
+//    p's score reads its two scales as one float2.
+// The query vector is stored with its dims in k_slot order: a lane's
+// m16n8k32 B registers for both k-steps are one 16-byte chunk.
 #pragma once
 
 #include <stdint.h>
@@ -28,9 +30,25 @@ constexpr int kVOffset = kKScaleOffset + kPagePositions * 4;                    
 constexpr int kVScaleOffset = kVOffset + kPagePositions * kHeadDim;                   // 8448
 
 __host__ __device__ __forceinline__ int k_slot(int d) { return ((d & 15) >> 2) * 16 + (d >> 4) * 4 + (d & 3); }
-__host__ __device__ __forceinline__ int v_slot(int p) {
-    return ((p & 7) >> 1) * 16 + (p >> 4) * 4 + ((p >> 3) & 1) * 2 + (p & 1);
+
+// Byte of element (row, col) of a 64x64 int8 matrix in m16n8k32 A-fragment
+// order: [16-row tile][32-col k-step][lane = 4*(row&7) + ((col>>2)&3)]
+// [register = (row>>3&1) + 2*(col>>4&1)][col&3].
+__host__ __device__ __forceinline__ int frag_byte(int row, int col) {
+    return (row >> 4) * 1024 + (col >> 5) * 512 + ((row & 7) * 4 + ((col >> 2) & 3)) * 16 +
+           (((row >> 3) & 1) + 2 * ((col >> 4) & 1)) * 4 + (col & 3);
 }
+// The QK step leaves position p's score with lane 4*(p&7) + (p>>4&3) (half
+// p>>3&1).  pv_col(p) is p's column in the PV product, chosen so that the
+// eight lanes sharing p>>4&3 hold exactly the sixteen positions of the
+// B fragment that lanes with that thread-in-group index read.
+__host__ __device__ __forceinline__ int pv_col(int p) {
+    const int g = p & 7;
+    return 32 * (g >> 2) + 16 * ((g >> 1) & 1) + 4 * ((p >> 4) & 3) + 2 * (g & 1) + ((p >> 3) & 1);
+}
+__host__ __device__ __forceinline__ int scale_slot(int p) { return 2 * ((p & 7) * 4 + ((p >> 4) & 3)) + ((p >> 3) & 1); }
+__host__ __device__ __forceinline__ int k_byte(int p, int d) { return frag_byte(p, d); }
+__host__ __device__ __forceinline__ int v_byte(int p, int d) { return kVOffset + frag_byte(d, pv_col(p)); }
 
 __host__ __device__ __forceinline__ size_t kv_page_bytes(int layers, int heads) {
     return (size_t)layers * heads * kKvBlockBytes;

@@ -291,13 +291,13 @@ __global__ void __launch_bounds__(256) kv_fill_kernel(uint64_t key, int layers, 
     const int j = pos % kPagePositions;
     uint8_t *blk = pool + (size_t)page * page_bytes + kv_block_offset(layer, head, heads);
     if (kind == 0) {
-        blk[j * kHeadDim + k_slot(lane)] = (uint8_t)q0;
-        blk[j * kHeadDim + k_slot(lane + 32)] = (uint8_t)q1;
-        if (lane == 0) reinterpret_cast<float *>(blk + kKScaleOffset)[j] = scale;
+        blk[k_byte(j, lane)] = (uint8_t)q0;
+        blk[k_byte(j, lane + 32)] = (uint8_t)q1;
+        if (lane == 0) reinterpret_cast<float *>(blk + kKScaleOffset)[scale_slot(j)] = scale;
     } else {
-        blk[kVOffset + lane * kHeadDim + v_slot(j)] = (uint8_t)(q0 + 128);
-        blk[kVOffset + (lane + 32) * kHeadDim + v_slot(j)] = (uint8_t)(q1 + 128);
-        if (lane == 0) reinterpret_cast<float *>(blk + kVScaleOffset)[j] = scale;
+        blk[v_byte(j, lane)] = (uint8_t)q0;
+        blk[v_byte(j, lane + 32)] = (uint8_t)q1;
+        if (lane == 0) reinterpret_cast<float *>(blk + kVScaleOffset)[scale_slot(j)] = scale;
     }
 }
 

@@ -7,15 +7,29 @@ BLOCK = 8704
 
 
 def k_slot(d):
+    """Storage byte of query dim d (the B-fragment order of both k-steps)."""
     return ((d & 15) >> 2) * 16 + (d >> 4) * 4 + (d & 3)
 
 
-def v_slot(p):
-    return ((p & 7) >> 1) * 16 + (p >> 4) * 4 + ((p >> 3) & 1) * 2 + (p & 1)
+def frag_byte(row, col):
+    """Byte of (row, col) of a 64x64 int8 matrix in m16n8k32 A-fragment order."""
+    return ((row >> 4) * 1024 + (col >> 5) * 512 + ((row & 7) * 4 + ((col >> 2) & 3)) * 16
+            + (((row >> 3) & 1) + 2 * ((col >> 4) & 1)) * 4 + (col & 3))
+
+
+def pv_col(p):
+    g = p & 7
+    return 32 * (g >> 2) + 16 * ((g >> 1) & 1) + 4 * ((p >> 4) & 3) + 2 * (g & 1) + ((p >> 3) & 1)
+
+
+def scale_slot(p):
+    return 2 * ((p & 7) * 4 + ((p >> 4) & 3)) + ((p >> 3) & 1)
 
 
 K_ORDER = np.array([k_slot(d) for d in range(64)])
-V_ORDER = np.array([v_slot(p) for p in range(64)])
+K_BYTE = np.array([[frag_byte(p, d) for d in range(64)] for p in range(64)])  # [position][dim] -> byte
+V_BYTE = np.array([[frag_byte(d, pv_col(p)) for d in range(64)] for p in range(64)])  # within the V block
+S_SLOT = np.array([scale_slot(p) for p in range(64)])
 
 
 def make_case(seed, lengths, heads, layers=2, layer=1, max_pages=17):
@@ -40,17 +54,17 @@ def make_case(seed, lengths, heads, layers=2, layer=1, max_pages=17):
             for h in range(heads):
                 base = page * page_bytes + (layer * heads + h) * BLOCK
                 blk = pool[base:base + BLOCK]
-                kr = np.zeros((64, 64), np.uint8)
-                kr[:cnt][:, K_ORDER] = K[s, lo:hi, h].view(np.uint8)
-                blk[:4096] = kr.reshape(-1)
+                kr = np.zeros(4096, np.uint8)
+                kr[K_BYTE[:cnt]] = K[s, lo:hi, h].view(np.uint8)
+                blk[:4096] = kr
                 ks = np.zeros(64, np.float32)
-                ks[:cnt] = KS[s, lo:hi, h]
+                ks[S_SLOT[:cnt]] = KS[s, lo:hi, h]
                 blk[4096:4352] = ks.view(np.uint8)
-                vt = np.full((64, 64), 128, np.uint8)
-                vt[:, V_ORDER[:cnt]] = (V[s, lo:hi, h].astype(np.int16) + 128).astype(np.uint8).T
-                blk[4352:8448] = vt.reshape(-1)
+                vt = np.zeros(4096, np.uint8)
+                vt[V_BYTE[:cnt]] = V[s, lo:hi, h].view(np.uint8)
+                blk[4352:8448] = vt
                 vs = np.zeros(64, np.float32)
-                vs[:cnt] = VS[s, lo:hi, h]
+                vs[S_SLOT[:cnt]] = VS[s, lo:hi, h]
                 blk[8448:8704] = vs.view(np.uint8)
     q_perm = np.zeros((rows, heads, 64), np.int8)
     q_perm[:, :, K_ORDER] = Q

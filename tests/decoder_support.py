@@ -2,6 +2,7 @@
 the CPU oracle and regenerate the synthetic prefix K/V on the host."""
 import numpy as np
 
+from attention_support import K_BYTE, S_SLOT, V_BYTE
 from conftest import entry
 
 KV_STREAM_SHIFT = 20
@@ -34,23 +35,11 @@ def prefix_kv(ops, oracle, decoder, kv, count, seed, session):
             kv[scales][layer, :count] = s.reshape(count, H)
 
 
-def k_slot(d):
-    return ((d & 15) >> 2) * 16 + (d >> 4) * 4 + (d & 3)
-
-
-def v_slot(p):
-    return ((p & 7) >> 1) * 16 + (p >> 4) * 4 + ((p >> 3) & 1) * 2 + (p & 1)
-
-
-K_ORDER = np.array([k_slot(d) for d in range(64)])  # storage byte of dim d in a K row
-V_ORDER = np.array([v_slot(p) for p in range(64)])  # storage byte of position p in a V^T row
-
-
 def read_slot_kv(engine, slot, positions):
     """Reads positions [0, positions) of a slot from the paged pool into the
     flat reference layout (k, v int8 [layers][positions][H*64]; ks, vs).
-    Page record of (layer, head): K rows with dims in K_ORDER, K scales,
-    V transposed (row = dim) with positions in V_ORDER holding v + 128, V scales."""
+    Page record of (layer, head): K and V^T int8 in m16n8k32 A-fragment
+    order (K_BYTE, V_BYTE), scales at S_SLOT."""
     cfg = engine.model
     H, L = cfg.heads, cfg.layers
     page_bytes = engine.page_bytes()
@@ -66,13 +55,10 @@ def read_slot_kv(engine, slot, positions):
         for l in range(L):
             for h in range(H):
                 blk = pool[page * page_bytes + (l * H + h) * 8704:][:8704]
-                krows = blk[:4096].reshape(64, 64)[:n]
-                out["k"][l, lo:hi, h * 64:(h + 1) * 64] = krows[:, K_ORDER].view(np.int8)
-                out["ks"][l, lo:hi, h] = blk[4096:4352].view(np.float32)[:n]
-                vt = blk[4352:8448].reshape(64, 64)  # [dim][slot]
-                v = (vt[:, V_ORDER[:n]].astype(np.int16) - 128).astype(np.int8)  # [dim][position]
-                out["v"][l, lo:hi, h * 64:(h + 1) * 64] = v.T
-                out["vs"][l, lo:hi, h] = blk[8448:8704].view(np.float32)[:n]
+                out["k"][l, lo:hi, h * 64:(h + 1) * 64] = blk[:4096][K_BYTE[:n]].view(np.int8)
+                out["ks"][l, lo:hi, h] = blk[4096:4352].view(np.float32)[S_SLOT[:n]]
+                out["v"][l, lo:hi, h * 64:(h + 1) * 64] = blk[4352:8448][V_BYTE[:n]].view(np.int8)
+                out["vs"][l, lo:hi, h] = blk[8448:8704].view(np.float32)[S_SLOT[:n]]
     return out
 
 
