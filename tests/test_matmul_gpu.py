@@ -64,7 +64,8 @@ def test_matmul_i8g32_bit_exact(ops, oracle, cuda, m, n, k):
 
 
 @pytest.mark.parametrize("m,n,k", [(64, 2048, 512), (128, 1536, 512), (200, 512, 2048), (512, 4096, 512),
-                                   (100, 96, 96), (129, 136, 160), (512, 8192, 512), (64, 8, 32)])
+                                   (100, 96, 96), (129, 136, 160), (512, 8192, 512), (64, 8, 32),
+                                   (96, 256, 4096)])
 def test_matmul_tcgen05_bit_exact(ops, oracle, cuda, m, n, k):
     """m >= 64 runs the tcgen05 kind::i8 GEMM: D and y identical to the oracle
     and to the GEMV (batch invariance across the two kernels)."""
@@ -85,8 +86,9 @@ def test_matmul_tcgen05_bit_exact(ops, oracle, cuda, m, n, k):
     assert np.array_equal(y16.cpu().numpy(), y[:16].cpu().numpy())
 
 
-def test_matmul_residual_and_ldy(ops, oracle, cuda):
-    m, n, k = 4, 96, 256
+@pytest.mark.parametrize("m", [4, 130])
+def test_matmul_residual_and_ldy(ops, oracle, cuda, m):
+    n, k = 96, 256
     x, w, sw = _inputs(ops, m, n, k, seed=9)
     q_ref, s_ref = oracle.quantize_rows(x)
     y_ref = oracle.matmul_i8g32(q_ref, s_ref, w, sw)
@@ -110,8 +112,9 @@ def test_matmul_residual_and_ldy(ops, oracle, cuda):
     assert np.array_equal(out.cpu().numpy(), res + y_ref)
 
 
-def test_matmul_batched_equals_single(ops, oracle, cuda):
-    m, n, k, b = 16, 256, 512, 3
+@pytest.mark.parametrize("m", [16, 96])
+def test_matmul_batched_equals_single(ops, oracle, cuda, m):
+    n, k, b = 256, 512, 3
     x, _, _ = _inputs(ops, m, n, k)
     q_ref, s_ref = oracle.quantize_rows(x)
     w = ops.synth_int8(5, 2, b * n * k).reshape(b, n, k)
