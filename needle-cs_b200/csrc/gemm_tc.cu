@@ -11,17 +11,21 @@
 // operand, so TMEM lane = output feature n and each epilogue thread owns
 // one n: its fp16 group scales are one contiguous row of sw and its stores
 // are coalesced across the warp.
-//  * warp 0 (one lane): TMA loads of the weight tile [128 rows][128 B] and
-//    the activation tile [BT rows][128 B] per stage (4 groups), 128-byte
-//    swizzle, 8-stage ring running ahead across tiles (no cluster multicast).
-//  * warp 1: allocates all 512 TMEM columns; one lane issues one
+//  * warp 0: TMA loads of the weight tile [128 rows][128 B] and the
+//    activation tile [BT rows][128 B] per stage (4 groups), 128-byte
+//    swizzle, running ahead across tiles (no cluster multicast).  Copies
+//    issued by one thread complete one after another, so every load in
+//    flight is issued by its own lane.
+//  * warp 1: allocates all 512 TMEM columns; elect.sync issues one
 //    tcgen05.mma kind::i8 (M 128, N BT, K 32) per 32-column group with
 //    accumulate off, so each accumulator holds exactly D of that group.  A
-//    stage's four groups fill one TMEM slot of a 512 / (4 BT)-slot ring.
+//    stage's four groups fill TMEM slot r of a 512 / (4 BT)-slot ring; one
+//    commit per stage both fills the slot and frees shared-memory stage r.
 //  * warps 2..17: epilogue, (TMEM lane quadrant) x (BT / 4 token columns).
 //    Per slot a thread reads its four groups' D, releases the slot and folds
-//    acc = fma(half(sw[n][g]), float(D), acc) in ascending group order; the
-//    token's activation scale multiplies once per tile.
+//    acc = fma(half(sw[n][g]), float(D), acc) in ascending group order, two
+//    tokens per packed f32x2 instruction; the token's activation scale
+//    multiplies once per tile.
 // Every wait is bounded; on a timeout the CTA records kStatusTimeout, leaves
 // its loops, frees TMEM and exits.
 #include <cudaTypedefs.h>
@@ -36,19 +40,20 @@ namespace ndl {
 
 constexpr int kTcBlockN = 128;  // weight rows per tile (MMA M, TMEM lanes)
 constexpr int kTcBlockK = 128;  // bytes per stage = 4 groups
-constexpr int kTcStages = 8;
 constexpr int kTcEpiWarps = 16;
 constexpr int kTcThreads = 64 + 32 * kTcEpiWarps;
 constexpr uint32_t kTcTmemCols = 512;
 constexpr int kTcWBytes = kTcBlockN * kTcBlockK;  // 16 KB
-constexpr uint32_t kTcWaitLimit = 1u << 26;
+constexpr uint32_t kTcWaitLimit = 1u << 22;  // tests of about a microsecond each: a few seconds
 
+// One stage of shared memory per TMEM slot (4 groups x BT columns), so the
+// MMA commit that fills slot r also frees stage r: S = 512 / (4 BT).
 template <int BT>
 struct TcSmem {
-    static constexpr int kSlots = kTcTmemCols / (4 * BT);
-    uint8_t w[kTcStages][kTcWBytes];      // 1024-byte aligned (swizzle atoms)
-    uint8_t x[kTcStages][BT * kTcBlockK];  // 2 or 4 KB: stays 1024-aligned
-    uint64_t full[kTcStages], empty[kTcStages], acc_full[kSlots], acc_empty[kSlots];
+    static constexpr int kStages = kTcTmemCols / (4 * BT);
+    uint8_t w[kStages][kTcWBytes];      // 1024-byte aligned (swizzle atoms)
+    uint8_t x[kStages][BT * kTcBlockK];  // 2 or 4 KB: stays 1024-aligned
+    uint64_t full[kStages], acc_full[kStages], acc_empty[kStages];
     uint32_t tmem_base;
     volatile int abort;
 };
@@ -89,13 +94,34 @@ __device__ __forceinline__ uint4 tc_scales8(const uint16_t *row, int c8, int G, 
     return make_uint4(h[0] | h[1] << 16, h[2] | h[3] << 16, h[4] | h[5] << 16, h[6] | h[7] << 16);
 }
 
+// Packed pairs of fp32 (fma/add.rn.f32x2: each half is an IEEE fma/add with
+// round-to-nearest, the same bits as the scalar forms).
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float &lo, float &hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
+
 template <int BT>
 __global__ void __launch_bounds__(kTcThreads, 1)
     gemm_i8g32_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x,
                          TcParams p) {
     constexpr int EC = BT / 4;  // token columns per epilogue warp
     constexpr int kSlotCols = 4 * BT;
-    constexpr int kSlots = TcSmem<BT>::kSlots;
+    constexpr int S = TcSmem<BT>::kStages;
     constexpr uint32_t kXBytes = BT * kTcBlockK;
     extern __shared__ uint8_t smem_raw[];
     TcSmem<BT> &s =
@@ -107,8 +133,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int tiles = p.batch * nblk * tblk;
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < kTcStages; i++) mbar_init(&s.full[i], 1), mbar_init(&s.empty[i], 1);
-        for (int i = 0; i < kSlots; i++) mbar_init(&s.acc_full[i], 1), mbar_init(&s.acc_empty[i], kTcEpiWarps);
+        for (int i = 0; i < S; i++)
+            mbar_init(&s.full[i], 1), mbar_init(&s.acc_full[i], 1), mbar_init(&s.acc_empty[i], kTcEpiWarps);
         s.abort = 0;
         fence_mbar_init();
         prefetch_tmap(&map_w);
@@ -124,98 +150,123 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const uint32_t tmem = s.tmem_base;
 
     if (warp == 0) {
-        if (lane == 0) {
-            uint32_t seq = 0;
-            for (int tile = blockIdx.x; tile < tiles && !s.abort; tile += gridDim.x) {
-                const TcTile tt = tc_tile(tile, nblk, tblk);
-                for (int st = 0; st < n_stages; st++, seq++) {
-                    const int r = seq % kTcStages;
-                    if (seq >= kTcStages && !tc_wait(s, &s.empty[r], ((seq / kTcStages) - 1) & 1)) break;
+        // Producer, warp-converged.  Copies issued by one thread complete one
+        // after another, so stage seq's weight and activation tiles are issued
+        // by lanes 2(seq % S) and 2(seq % S) + 1: every load in flight has its
+        // own thread.  Stage r is reused once the MMAs that read it committed
+        // (acc_full[r]).
+        uint32_t seq = 0;
+        for (int tile = blockIdx.x; tile < tiles && !s.abort; tile += gridDim.x) {
+            const TcTile tt = tc_tile(tile, nblk, tblk);
+            for (int st = 0; st < n_stages; st++, seq++) {
+                const int r = seq % S;
+                if (seq >= (uint32_t)S && !tc_wait(s, &s.acc_full[r], ((seq / S) - 1) & 1)) break;
+                const int lw = 2 * r;
+                if (lane == lw) {
                     mbar_arrive_expect_tx(&s.full[r], kTcWBytes + kXBytes);
                     tma_load_3d(s.w[r], &map_w, st * kTcBlockK, tt.n0, tt.bz, &s.full[r]);
+                } else if (lane == lw + 1) {
                     tma_load_2d(s.x[r], &map_x, st * kTcBlockK, tt.tb * BT, &s.full[r]);
                 }
+                __syncwarp();
             }
         }
     } else if (warp == 1) {
-        if (lane == 0) {
-            const uint32_t idesc = idesc_i8(kTcBlockN, BT);
-            uint32_t seq = 0;
-            for (int tile = blockIdx.x; tile < tiles && !s.abort; tile += gridDim.x) {
-                for (int st = 0; st < n_stages && !s.abort; st++, seq++) {
-                    const int r = seq % kTcStages, slot = seq % kSlots;
-                    if (!tc_wait(s, &s.full[r], (seq / kTcStages) & 1)) break;
-                    if (seq >= (uint32_t)kSlots && !tc_wait(s, &s.acc_empty[slot], ((seq / kSlots) - 1) & 1)) break;
-                    tc_fence_after();
-                    const uint64_t dw = sw128_kmajor_desc(s.w[r]), dx = sw128_kmajor_desc(s.x[r]);
-                    const int groups = min(4, G - 4 * st);
-                    for (int j = 0; j < groups; j++)
-                        mma_i8(tmem + (uint32_t)(slot * kSlotCols + j * BT), dw + (uint64_t)(j * 2),
-                               dx + (uint64_t)(j * 2), idesc, 0u);
-                    mma_commit(&s.acc_full[slot]);
-                    mma_commit(&s.empty[r]);
-                }
+        // MMA issuer, warp-converged with elect.sync: one commit per stage
+        const uint32_t idesc = idesc_i8(kTcBlockN, BT);
+        uint32_t seq = 0;
+        for (int tile = blockIdx.x; tile < tiles && !s.abort; tile += gridDim.x) {
+            for (int st = 0; st < n_stages && !s.abort; st++, seq++) {
+                const int r = seq % S;
+                if (!tc_wait(s, &s.full[r], (seq / S) & 1)) break;
+                if (seq >= (uint32_t)S && !tc_wait(s, &s.acc_empty[r], ((seq / S) - 1) & 1)) break;
+                __syncwarp();
+                tc_fence_after();
+                const uint64_t dw = sw128_kmajor_desc(s.w[r]), dx = sw128_kmajor_desc(s.x[r]);
+                const int groups = min(4, G - 4 * st);
+                for (int j = 0; j < groups; j++)
+                    mma_i8_elect(tmem + (uint32_t)(r * kSlotCols + j * BT), dw + (uint64_t)(j * 2),
+                                 dx + (uint64_t)(j * 2), idesc);
+                mma_commit_elect(&s.acc_full[r]);
             }
         }
     } else {
         const int quad = warp & 3, c0 = ((warp - 2) >> 2) * EC;
         const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)c0;
         const bool vec = p.sw_vec != 0;
+        const uint64_t neg_magic = f2_pack(-12582912.0f, -12582912.0f);
         uint32_t seq = 0;
         bool ok = true;
+        // first scale chunk of the next tile, loaded one tile ahead
+        uint4 sc_first = make_uint4(0u, 0u, 0u, 0u);
+        if ((int)blockIdx.x < tiles) {
+            const TcTile t0 = tc_tile(blockIdx.x, nblk, tblk);
+            const int n = min(t0.n0 + quad * 32 + lane, p.n - 1);
+            sc_first = tc_scales8(p.sw + (long long)t0.bz * p.sw_stride + (size_t)n * G, 0, G, vec);
+        }
         for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
             const TcTile tt = tc_tile(tile, nblk, tblk);
             const int n = tt.n0 + quad * 32 + lane;
             const bool nv = n < p.n;
             const uint16_t *srow = p.sw + (long long)tt.bz * p.sw_stride + (size_t)(nv ? n : 0) * G;
-            uint4 sc = tc_scales8(srow, 0, G, vec);
+            uint4 sc = sc_first;
             uint4 sc_next = G > 8 ? tc_scales8(srow, 8, G, vec) : make_uint4(0u, 0u, 0u, 0u);
-            float acc[EC];
+            if (tile + (int)gridDim.x < tiles) {
+                const TcTile tn = tc_tile(tile + gridDim.x, nblk, tblk);
+                const int nn = min(tn.n0 + quad * 32 + lane, p.n - 1);
+                sc_first = tc_scales8(p.sw + (long long)tn.bz * p.sw_stride + (size_t)nn * G, 0, G, vec);
+            }
+            // this tile's activation scales and residuals, needed at the end
+            float sa[EC], res[EC];
 #pragma unroll
-            for (int c = 0; c < EC; c++) acc[c] = 0.0f;
+            for (int c = 0; c < EC; c++) {
+                const int t = tt.tb * BT + c0 + c;
+                const bool ok_t = t < p.m && nv;
+                sa[c] = ok_t ? __ldg(p.sa + t) : 0.0f;
+                res[c] = ok_t && p.residual ? p.residual[(size_t)t * p.ldy + n] : 0.0f;
+            }
+            uint64_t acc[EC / 2];
+#pragma unroll
+            for (int c = 0; c < EC / 2; c++) acc[c] = 0ull;
             for (int st = 0; st < n_stages; st++, seq++) {
-                const int slot = seq % kSlots;
-                if (!tc_wait(s, &s.acc_full[slot], (seq / kSlots) & 1)) {
+                const int r = seq % S;
+                if (!tc_wait(s, &s.acc_full[r], (seq / S) & 1)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
                 const int groups = min(4, G - 4 * st);
+                // all four groups' D in registers with one wait, then the slot is released
+                uint32_t d[4][EC];
+#pragma unroll
+                for (int j = 0; j < 4; j++)
+                    if (j < groups) tmem_ld<EC>(lane_base + (uint32_t)(r * kSlotCols + j * BT), d[j]);
+                tmem_ld_wait();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&s.acc_empty[r]);
                 // scales of groups 4st..4st+3: half (st & 1) of the current 8-group chunk
                 const uint32_t w01 = (st & 1) ? sc.z : sc.x, w23 = (st & 1) ? sc.w : sc.y;
-                // two groups at a time (2 x EC registers of D); the slot is
-                // released once all four are in registers
 #pragma unroll
-                for (int h = 0; h < 2; h++) {
-                    uint32_t d[2][EC];
+                for (int j = 0; j < 4; j++) {
+                    if (j >= groups) break;
+                    const uint32_t hw = j < 2 ? w01 : w23;
+                    const float scale = half_to_float_ref_fast((uint16_t)((j & 1) ? hw >> 16 : hw & 0xFFFFu));
+                    const uint64_t sc2 = f2_pack(scale, scale);
+                    // acc = fma(sw, float(D), acc); float(D) exact by the 1.5*2^23 trick
 #pragma unroll
-                    for (int jj = 0; jj < 2; jj++)
-                        if (2 * h + jj < groups)
-                            tmem_ld<EC>(lane_base + (uint32_t)(slot * kSlotCols + (2 * h + jj) * BT), d[jj]);
-                    tmem_ld_wait();
-                    if (h == 1) {
-                        tc_fence_before();
-                        __syncwarp();
-                        if (lane == 0) mbar_arrive(&s.acc_empty[slot]);
+                    for (int c = 0; c < EC / 2; c++) {
+                        const uint64_t dv = f2_add(f2_pack(__int_as_float((int)d[j][2 * c] + 0x4B400000),
+                                                           __int_as_float((int)d[j][2 * c + 1] + 0x4B400000)),
+                                                   neg_magic);
+                        acc[c] = f2_fma(sc2, dv, acc[c]);
                     }
-                    const uint32_t hw = h ? w23 : w01;
+                    if (p.acc && nv) {  // optional int32 accumulator output (parity checks)
+                        const int g = 4 * st + j;
 #pragma unroll
-                    for (int jj = 0; jj < 2; jj++) {
-                        const int j = 2 * h + jj;
-                        if (j >= groups) break;
-                        const float scale = half_to_float_ref_fast((uint16_t)(jj ? hw >> 16 : hw & 0xFFFFu));
-                        // acc = fma(sw, float(D), acc); float(D) exact by the 1.5*2^23 trick
-#pragma unroll
-                        for (int c = 0; c < EC; c++)
-                            acc[c] = __fmaf_rn(scale, __int_as_float((int)d[jj][c] + 0x4B400000) - 12582912.0f,
-                                               acc[c]);
-                        if (p.acc && nv) {  // optional int32 accumulator output (parity checks)
-                            const int g = 4 * st + j;
-#pragma unroll
-                            for (int c = 0; c < EC; c++) {
-                                const int t = tt.tb * BT + c0 + c;
-                                if (t < p.m) p.acc[((size_t)t * p.n + n) * G + g] = (int)d[jj][c];
-                            }
+                        for (int c = 0; c < EC; c++) {
+                            const int t = tt.tb * BT + c0 + c;
+                            if (t < p.m) p.acc[((size_t)t * p.n + n) * G + g] = (int)d[j][c];
                         }
                     }
                 }
@@ -229,12 +280,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             if (nv) {
                 float *y = p.y + (long long)tt.bz * p.y_stride;
 #pragma unroll
-                for (int c = 0; c < EC; c++) {
-                    const int t = tt.tb * BT + c0 + c;
-                    if (t < p.m) {
-                        const float v = __fmul_rn(acc[c], __ldg(p.sa + t));
-                        const size_t o = (size_t)t * p.ldy + n;
-                        y[o] = p.residual ? __fadd_rn(p.residual[o], v) : v;
+                for (int c = 0; c < EC / 2; c++) {
+                    float v[2];
+                    f2_unpack(acc[c], v[0], v[1]);
+#pragma unroll
+                    for (int e = 0; e < 2; e++) {
+                        const int t = tt.tb * BT + c0 + 2 * c + e;
+                        if (t < p.m) {
+                            const float out = __fmul_rn(v[e], sa[2 * c + e]);
+                            y[(size_t)t * p.ldy + n] = p.residual ? __fadd_rn(res[2 * c + e], out) : out;
+                        }
                     }
                 }
             }

@@ -87,16 +87,21 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
         "l"(src), "r"(bytes), "r"(smem_u32(bar))
         : "memory");
 }
+// One test of the phase.  While it is incomplete the thread is suspended
+// (not spinning) until the phase completes or about kWaitHintNs pass, so
+// waiting warps leave the issue slots to the working ones.
+constexpr uint32_t kWaitHintNs = 1000;
 __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
         : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(kWaitHintNs)
         : "memory");
     return ok != 0;
 }
-// Bounded wait: gives up after `limit` polls and reports false.
+// Bounded wait: gives up after `limit` tests (each at most about
+// kWaitHintNs) and reports false.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity, uint32_t limit) {
     for (uint32_t i = 0; i < limit; i++)
         if (mbar_try_wait(bar, parity)) return true;

@@ -61,6 +61,23 @@ __device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t a_desc, uint64_
         "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
+// Warp-converged forms: every lane executes the call, elect.sync picks one
+// lane (the same lane every time: the lowest active one) to issue, so the
+// warp's control flow and the instruction's operands stay uniform.
+// D = A x B with accumulate off (the enable-input-d predicate is false).
+__device__ __forceinline__ void mma_i8_elect(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc) {
+    asm volatile(
+        "{\n .reg .pred e, acc;\n elect.sync _|e, 0xffffffff;\n setp.ne.b32 acc, %4, 0;\n"
+        " @e tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, acc;\n}\n" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(0u)
+        : "memory");
+}
+__device__ __forceinline__ void mma_commit_elect(uint64_t *bar) {
+    asm volatile(
+        "{\n .reg .pred e;\n elect.sync _|e, 0xffffffff;\n"
+        " @e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n}\n" ::"r"(smem_u32(bar))
+        : "memory");
+}
 // Arrives on `bar` once every tcgen05 op this thread issued has completed.
 __device__ __forceinline__ void mma_commit(uint64_t *bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
