@@ -280,6 +280,61 @@ NDL_API int ndl_sample_argmax(ndl_engine *e, const uint32_t *masks, int words, i
  * head row: ids/log_probs/probs [heads][k], k <= 8; probs nullable. */
 NDL_API int ndl_sample_topk(ndl_engine *e, int k, int mask_special_023, int *ids, float *log_probs, float *probs);
 
+/* Per-slot vocabulary masks kept on the device, for callers that reuse one
+ * mask for every step of a request (the reference's lanes keep their masks,
+ * src/Needle/BatchedSession.cs:310-330).  set_mask: `words` uint32 words,
+ * ids >= 32*words disallowed; NULL clears the slot's mask.
+ * sample_argmax_slots: ArgMaxMasked on every head row of the last step with
+ * the stored mask of slots[h] (negative or unmasked slot: no mask). */
+NDL_API int ndl_engine_set_mask(ndl_engine *e, int slot, const uint32_t *mask, int words);
+NDL_API int ndl_sample_argmax_slots(ndl_engine *e, const int *slots, int *ids, float *probs);
+
+/* Engine limits. */
+typedef struct {
+    int slots, capacity, vocab, max_rows, max_heads, layers, dim, heads;
+} ndl_engine_info;
+NDL_API int ndl_engine_get_info(ndl_engine *e, ndl_engine_info *info);
+
+/* ------------------------------------------------------------------ */
+/* Continuous batching (replaces BatchedSession.RunBatch's loop,       */
+/* src/Needle/BatchedSession.cs:218-268)                               */
+/* ------------------------------------------------------------------ */
+/* Each step packs every running request's decode row, then prompt chunks
+ * (at most prefill_chunk positions of one request per step) up to max_rows,
+ * runs one ndl_forward_batch and samples every head row with the request's
+ * mask.  A request's tokens equal those it gets alone (rows are batch
+ * invariant).  One host thread per scheduler. */
+typedef struct ndl_sched ndl_sched;
+typedef struct {
+    int max_rows;      /* rows per step, <= the engine's max_rows and max_heads */
+    int prefill_chunk; /* prompt positions of one request per step */
+} ndl_sched_config;
+typedef struct {
+    int request;
+    int kind;   /* 1: first token produced, 2: request finished */
+    int token;  /* the token of this step (-1 if none) */
+    int status; /* kind 2: 0 or a FailureReason (3 = ContextExhausted) */
+} ndl_sched_event;
+NDL_API int ndl_sched_create(ndl_engine *e, const ndl_sched_config *cfg, ndl_sched **out);
+/* A scheduler without an engine: plans steps and returns token
+ * (request * 7919 + produced) % vocab; for testing the packing on a host. */
+NDL_API int ndl_sched_create_dry(const ndl_sched_config *cfg, int slots, int capacity, int vocab, ndl_sched **out);
+NDL_API int ndl_sched_destroy(ndl_sched *s);
+/* Queues a request (arrival order = admission order).  mask: `mask_words`
+ * words, NULL = unmasked; stop_token < 0: none; generation ends after
+ * max_new_tokens tokens or the stop token. */
+NDL_API int ndl_sched_submit(ndl_sched *s, int request, const int32_t *prompt, int prompt_len, int max_new_tokens,
+                             int stop_token, const uint32_t *mask, int mask_words);
+/* Runs one step (none if nothing is queued or running): events of this step
+ * (at most `capacity` written, *count = all), rows and decode rows packed. */
+NDL_API int ndl_sched_step(ndl_sched *s, ndl_sched_event *events, int capacity, int *count, int *rows,
+                           int *decode_rows);
+/* Tokens produced so far by a request (capacity entries at most; *count = all). */
+NDL_API int ndl_sched_tokens(ndl_sched *s, int request, int32_t *tokens, int capacity, int *count);
+NDL_API int ndl_sched_pending(ndl_sched *s, int *waiting, int *running);
+/* The last step's packing (arrays of max_rows, nullable). */
+NDL_API int ndl_sched_last_plan(ndl_sched *s, int *tokens, int *row_slots, int *rows, int *head_rows, int *heads);
+
 #ifdef __cplusplus
 }
 #endif

@@ -58,6 +58,17 @@ SIGNATURES = {
     "ndl_batch_logits_row": (c_int, [c_void_p, c_int, c_void_p]),
     "ndl_sample_argmax": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p]),
     "ndl_sample_topk": (c_int, [c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p]),
+    "ndl_engine_set_mask": (c_int, [c_void_p, c_int, c_void_p, c_int]),
+    "ndl_sample_argmax_slots": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p]),
+    "ndl_engine_get_info": (c_int, [c_void_p, c_void_p]),
+    "ndl_sched_create": (c_int, [c_void_p, c_void_p, c_void_p]),
+    "ndl_sched_create_dry": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p]),
+    "ndl_sched_destroy": (c_int, [c_void_p]),
+    "ndl_sched_submit": (c_int, [c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_void_p, c_int]),
+    "ndl_sched_step": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_void_p]),
+    "ndl_sched_tokens": (c_int, [c_void_p, c_int, c_void_p, c_int, c_void_p]),
+    "ndl_sched_pending": (c_int, [c_void_p, c_void_p, c_void_p]),
+    "ndl_sched_last_plan": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
     "ndl_engine_profile": (c_int, [c_void_p, c_int]),
     "ndl_engine_use_graphs": (c_int, [c_void_p, c_int]),
     "ndl_engine_profile_read": (c_int, [c_void_p, c_void_p, c_void_p, c_int]),
@@ -71,6 +82,22 @@ class DecoderConfig(ctypes.Structure):
     """ndl_decoder_config."""
     _fields_ = [("layers", c_int), ("dim", c_int), ("heads", c_int), ("head_dim", c_int), ("ffn", c_int),
                 ("vocab", c_int), ("rope_theta", c_float), ("seed", c_u64)]
+
+
+class EngineInfo(ctypes.Structure):
+    """ndl_engine_info."""
+    _fields_ = [("slots", c_int), ("capacity", c_int), ("vocab", c_int), ("max_rows", c_int), ("max_heads", c_int),
+                ("layers", c_int), ("dim", c_int), ("heads", c_int)]
+
+
+class SchedConfig(ctypes.Structure):
+    """ndl_sched_config."""
+    _fields_ = [("max_rows", c_int), ("prefill_chunk", c_int)]
+
+
+class SchedEvent(ctypes.Structure):
+    """ndl_sched_event."""
+    _fields_ = [("request", c_int), ("kind", c_int), ("token", c_int), ("status", c_int)]
 
 
 class EngineConfig(ctypes.Structure):

@@ -28,8 +28,9 @@ int launch_step_prepare(const int32_t *updates, int32_t *page_table, int max_pag
 int launch_swiglu_quantize(const float *gu, int rows, int ffn, float *act, int8_t *q, float *scales,
                            cudaStream_t stream);
 int launch_gather_rows(const float *x, const int32_t *idx, int n, int dim, float *out, cudaStream_t stream);
-int launch_argmax_masked(const float *x, long long ldx, const uint32_t *mask, int words, long long ldm, int length,
-                         int rows, int32_t *ids, float *probs, cudaStream_t stream);
+int launch_argmax_masked(const float *x, long long ldx, const uint32_t *mask, int words, long long ldm,
+                         const int32_t *mask_index, int length, int rows, int32_t *ids, float *probs,
+                         cudaStream_t stream);
 int launch_topk_logsoftmax(const float *x, long long ldx, int n, int k, int mask023, int rows, int32_t *idx,
                            float *logp, float *probs, cudaStream_t stream);
 int launch_kv_fill(uint64_t seed, uint64_t session, int layers, int heads, int first, int count,
@@ -86,6 +87,11 @@ struct ndl_engine {
     int32_t *d_ids = nullptr;
     float *d_probs = nullptr, *d_logp = nullptr;
     uint32_t *d_masks = nullptr;
+    // per-slot sampling masks held on the device ([slots][vocab words]),
+    // allocated by the first ndl_engine_set_mask
+    uint32_t *d_mask_table = nullptr;
+    int32_t *d_mask_index = nullptr;
+    std::vector<char> slot_has_mask;
     void *h_out = nullptr;  // pinned sampling results
     int last_rows = 0, last_heads = 0;
     int max_chunks_cap = 0;
@@ -782,8 +788,70 @@ NDL_API int ndl_sample_argmax(ndl_engine *e, const uint32_t *masks, int words, i
     }
     {
         ProfScope p(e, NDL_PROF_SAMPLE);
-        TRY(launch_argmax_masked(e->logits, V, masks ? e->d_masks : nullptr, words, words, V, n, e->d_ids,
+        TRY(launch_argmax_masked(e->logits, V, masks ? e->d_masks : nullptr, words, words, nullptr, V, n, e->d_ids,
                                  probs ? e->d_probs : nullptr, s));
+    }
+    NDL_CUDA(cudaMemcpyAsync(h, e->d_ids, (size_t)n * 4, cudaMemcpyDeviceToHost, s));
+    if (probs) NDL_CUDA(cudaMemcpyAsync(h + (size_t)n * 4, e->d_probs, (size_t)n * 4, cudaMemcpyDeviceToHost, s));
+    TRY(check_status(e));
+    memcpy(ids, h, (size_t)n * 4);
+    if (probs) memcpy(probs, h + (size_t)n * 4, (size_t)n * 4);
+    return NDL_OK;
+}
+
+NDL_API int ndl_engine_get_info(ndl_engine *e, ndl_engine_info *info) {
+    NDL_REQUIRE(e && info, "null argument");
+    *info = ndl_engine_info{e->ec.slots, e->ec.capacity, e->dc.vocab, e->ec.max_rows, e->ec.max_heads,
+                            e->dc.layers, e->dc.dim, e->dc.heads};
+    return NDL_OK;
+}
+
+// Stores a vocabulary bitmask for `slot` on the device (NULL clears it):
+// the scheduler uploads a request's mask once instead of every step.
+NDL_API int ndl_engine_set_mask(ndl_engine *e, int slot, const uint32_t *mask, int words) {
+    NDL_REQUIRE(e, "null engine");
+    TRY(check_slot(e, slot));
+    const int max_words = (e->dc.vocab + 31) / 32;
+    if (!mask) {
+        if (!e->slot_has_mask.empty()) e->slot_has_mask[slot] = 0;
+        return NDL_OK;
+    }
+    NDL_REQUIRE(words >= 1 && words <= max_words, "words %d outside 1..%d", words, max_words);
+    if (!e->d_mask_table) {
+        TRY(dalloc(e, &e->d_mask_table, (size_t)e->ec.slots * max_words));
+        TRY(dalloc(e, &e->d_mask_index, (size_t)e->ec.max_heads));
+        e->slot_has_mask.assign(e->ec.slots, 0);
+    }
+    uint32_t *row = e->d_mask_table + (size_t)slot * max_words;
+    NDL_CUDA(cudaMemsetAsync(row, 0, (size_t)max_words * 4, e->stream));
+    // pageable source: the copy completes before the call returns
+    NDL_CUDA(cudaMemcpyAsync(row, mask, (size_t)words * 4, cudaMemcpyHostToDevice, e->stream));
+    NDL_CUDA(cudaStreamSynchronize(e->stream));
+    e->slot_has_mask[slot] = 1;
+    return NDL_OK;
+}
+
+// ArgMaxMasked over every head row of the last step, each row masked by the
+// stored mask of slots[h] (negative, or a slot without a mask: unmasked).
+NDL_API int ndl_sample_argmax_slots(ndl_engine *e, const int *slots, int *ids, float *probs) {
+    NDL_REQUIRE(e && slots && ids, "null argument");
+    const int n = e->last_heads, V = e->dc.vocab, max_words = (V + 31) / 32;
+    if (n == 0) return NDL_OK;
+    cudaStream_t s = e->stream;
+    uint8_t *h = static_cast<uint8_t *>(e->h_out);
+    int32_t *hidx = reinterpret_cast<int32_t *>(h + (size_t)e->ec.max_heads * 96);
+    bool any = false;
+    for (int i = 0; i < n; i++) {
+        const int sl = slots[i];
+        NDL_REQUIRE(sl < e->ec.slots, "head %d: slot %d out of range", i, sl);
+        hidx[i] = (sl >= 0 && !e->slot_has_mask.empty() && e->slot_has_mask[sl]) ? sl : -1;
+        any = any || hidx[i] >= 0;
+    }
+    if (any) NDL_CUDA(cudaMemcpyAsync(e->d_mask_index, hidx, (size_t)n * 4, cudaMemcpyHostToDevice, s));
+    {
+        ProfScope p(e, NDL_PROF_SAMPLE);
+        TRY(launch_argmax_masked(e->logits, V, any ? e->d_mask_table : nullptr, max_words, max_words,
+                                 any ? e->d_mask_index : nullptr, V, n, e->d_ids, probs ? e->d_probs : nullptr, s));
     }
     NDL_CUDA(cudaMemcpyAsync(h, e->d_ids, (size_t)n * 4, cudaMemcpyDeviceToHost, s));
     if (probs) NDL_CUDA(cudaMemcpyAsync(h + (size_t)n * 4, e->d_probs, (size_t)n * 4, cudaMemcpyDeviceToHost, s));

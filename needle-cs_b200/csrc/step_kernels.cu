@@ -110,16 +110,19 @@ int launch_gather_rows(const float *x, const int32_t *idx, int n, int dim, float
 // One CTA per row; mask may be NULL (all allowed) and is indexed per row.
 __global__ void __launch_bounds__(256) argmax_masked_kernel(const float *__restrict__ x, long long ldx,
                                                             const uint32_t *__restrict__ mask, int words,
-                                                            long long ldm, int length, int rows,
-                                                            int32_t *__restrict__ ids, float *__restrict__ probs) {
+                                                            long long ldm, const int32_t *__restrict__ mask_index,
+                                                            int length, int rows, int32_t *__restrict__ ids,
+                                                            float *__restrict__ probs) {
     __shared__ float s_val[256];
     __shared__ int s_idx[256];
     __shared__ float s_sum[256];
     const int row = blockIdx.x;
     if (row >= rows) return;
     const float *xr = x + (size_t)row * ldx;
-    const uint32_t *mr = mask ? mask + (size_t)row * ldm : nullptr;
-    const int limit = mask ? min(length, words * 32) : length;
+    // mask row: row itself, or mask_index[row] (negative: no mask)
+    const long long mrow = mask_index ? (long long)mask_index[row] : (long long)row;
+    const uint32_t *mr = mask && mrow >= 0 ? mask + mrow * ldm : nullptr;
+    const int limit = mr ? min(length, words * 32) : length;
     float best = -INFINITY;
     int best_i = -1;
     for (int i = threadIdx.x; i < limit; i += blockDim.x) {
@@ -168,10 +171,11 @@ __global__ void __launch_bounds__(256) argmax_masked_kernel(const float *__restr
     if (threadIdx.x == 0) ids[row] = arg;
 }
 
-int launch_argmax_masked(const float *x, long long ldx, const uint32_t *mask, int words, long long ldm, int length,
-                         int rows, int32_t *ids, float *probs, cudaStream_t stream) {
+int launch_argmax_masked(const float *x, long long ldx, const uint32_t *mask, int words, long long ldm,
+                         const int32_t *mask_index, int length, int rows, int32_t *ids, float *probs,
+                         cudaStream_t stream) {
     if (rows == 0) return NDL_OK;
-    argmax_masked_kernel<<<rows, 256, 0, stream>>>(x, ldx, mask, words, ldm, length, rows, ids, probs);
+    argmax_masked_kernel<<<rows, 256, 0, stream>>>(x, ldx, mask, words, ldm, mask_index, length, rows, ids, probs);
     return check_launch("argmax_masked");
 }
 

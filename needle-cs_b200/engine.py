@@ -143,6 +143,25 @@ class BatchedEngine:
             call("ndl_sample_argmax", self._h, None, 0, ids.ctypes.data, probs.ctypes.data if with_probs else None)
         return (ids, probs) if with_probs else ids
 
+    def set_mask(self, slot, mask=None):
+        """Keeps a vocabulary bitmask for `slot` on the device (None clears it)."""
+        if mask is None:
+            call("ndl_engine_set_mask", self._h, slot, None, 0)
+            return
+        m = np.ascontiguousarray(mask, dtype=np.uint32)
+        call("ndl_engine_set_mask", self._h, slot, m.ctypes.data, m.size)
+
+    def sample_argmax_slots(self, slots, with_probs=False):
+        """ArgMaxMasked of every head row with the stored mask of slots[h]."""
+        n = self._last_heads
+        sl = _i32(slots)
+        assert sl.size == n, (sl.size, n)
+        ids = np.empty(n, np.int32)
+        probs = np.empty(n, np.float32) if with_probs else None
+        call("ndl_sample_argmax_slots", self._h, sl.ctypes.data, ids.ctypes.data,
+             probs.ctypes.data if with_probs else None)
+        return (ids, probs) if with_probs else ids
+
     def sample_topk(self, k, mask_special_023=False, with_probs=False):
         n = self._last_heads
         ids = np.empty((n, k), np.int32)
