@@ -335,7 +335,166 @@ class DecodeWorkload:
                                  f"{int(lengths[:n].max())}), {threads} threads of the scalar C restatement")
 
 
-WORKLOADS = {"cfg1": GemvWorkload, "cfg2": DecodeWorkload, "cfg5": DecodeWorkload}
+class ServingWorkload:
+    """cfg3: continuous batching of 256 requests arriving as a Poisson process
+    (mean gap 2 ms), prompts U[32,384] ids U[0,8192), outputs U[8,96] tokens,
+    each with its own fixed vocabulary bitmask (30% of the bits set), on the
+    12-layer synthetic decoder.  Steps pack decode rows first, then prompt
+    chunks of at most 256 positions, up to 512 rows (ndl_sched_*).  Requests
+    are submitted when the wall clock passes their arrival time; value is the
+    output tokens per second of the makespan (first arrival to last token),
+    with TTFT (arrival to first token) and goodput (requests per second whose
+    TTFT met the SLO) beside it.  Per-(rows, heads) graphs are off: mixed
+    steps rarely repeat a shape."""
+
+    name = "cfg3_serving"
+
+    def __init__(self, n_requests=256, mean_gap_ms=2.0, seed=3, ttft_slo_ms=250.0):
+        self.n, self.gap, self.seed, self.slo = n_requests, mean_gap_ms, seed, ttft_slo_ms
+        self.unit_bytes = None
+
+    def trace(self, rank=0, n=None, seed=None):
+        n = n or self.n
+        rng = np.random.default_rng((seed if seed is not None else self.seed) + 7919 * rank)
+        arrivals = np.cumsum(rng.exponential(self.gap * 1e-3, n))
+        arrivals -= arrivals[0]
+        prompts = [rng.integers(0, 8192, int(rng.integers(32, 385))).astype(np.int32) for _ in range(n)]
+        outs = [int(rng.integers(8, 97)) for _ in range(n)]
+        masks = []
+        for _ in range(n):
+            bits = rng.random(8192) < 0.3
+            masks.append(np.packbits(bits.reshape(-1, 32)[:, ::-1], axis=1, bitorder="big").view(">u4")
+                         .astype(np.uint32).ravel())
+        return arrivals, prompts, outs, masks
+
+    def setup(self, device, rank=0, world=1):
+        eng_mod = __import__("needle_cs_b200.engine", fromlist=["engine"])
+        sch = __import__("needle_cs_b200.scheduler", fromlist=["scheduler"])
+        self.sched_mod = sch
+        self.engine = eng_mod.BatchedEngine(eng_mod.SyntheticDecoder(seed=1), slots=self.n, context_length=512,
+                                            chunk_size=512, max_heads=512, device=device.index or 0)
+        self.engine.use_graphs(False)
+        self.rank = rank
+
+    def serve(self, arrivals, prompts, outs, masks, id_base=0):
+        sched = self.sched_mod.Scheduler(self.engine, max_rows=512, prefill_chunk=256)
+        n = len(prompts)
+        first, done, steps, rows_total, dec_total = {}, {}, 0, 0, 0
+        t0 = time.perf_counter()
+        nxt = 0
+        while len(done) < n:
+            now = time.perf_counter() - t0
+            while nxt < n and arrivals[nxt] <= now:
+                sched.submit(id_base + nxt, prompts[nxt], outs[nxt], mask=masks[nxt])
+                nxt += 1
+            w, r = sched.pending()
+            if w == 0 and r == 0:
+                time.sleep(max(0.0, min(arrivals[nxt] - now, 0.001)))
+                continue
+            ev, rows, dec = sched.step()
+            t = time.perf_counter() - t0
+            steps += 1
+            rows_total += rows
+            dec_total += dec
+            for rid, kind, tok, st in ev:
+                if kind == self.sched_mod.FIRST_TOKEN:
+                    first[rid - id_base] = t
+                elif kind == self.sched_mod.FINISHED:
+                    done[rid - id_base] = (t, st)
+        makespan = max(t for t, _ in done.values())
+        out_tokens = sum(len(sched.tokens(id_base + i)) for i in range(n))
+        sched.close()
+        ttft = np.array([(first[i] - arrivals[i]) * 1e3 for i in range(n) if i in first])
+        ok = sum(1 for i in range(n) if i in first and (first[i] - arrivals[i]) * 1e3 <= self.slo
+                 and done[i][1] == 0)
+        return dict(makespan_s=makespan, out_tokens=out_tokens, steps=steps, rows=rows_total, decode_rows=dec_total,
+                    ttft_ms=ttft, good=ok, failed=sum(1 for t, st in done.values() if st != 0))
+
+    def describe(self):
+        return {"workload": self.name, "model": "synthetic needle-3-shaped decoder: 12 layers, d 512, 8x64 heads, "
+                                                "SwiGLU 2048, vocab 8192, int8 weights + fp16 per-32 scales",
+                "requests": self.n, "arrivals": f"Poisson, mean gap {self.gap} ms", "prompt_len": [32, 384],
+                "output_len": [8, 96], "mask": "per-request fixed bitmask, 30% of 8192 ids",
+                "max_rows_per_step": 512, "prefill_chunk": 256, "ttft_slo_ms": self.slo, "greedy": True,
+                "l2": "paged KV and weights stream per step; no L2 flush needed for a serving trace"}
+
+    def cpu_sample(self, oracle, arrivals, prompts, outs, threads=None):
+        """Oracle rows per second (one decoder row per prompt or output
+        position, all host cores) on a bounded sample, turned into the output
+        tokens per second of serving the same trace back to back."""
+        from concurrent.futures import ThreadPoolExecutor
+
+        syn = __import__("needle_cs_b200.synthetic", fromlist=["synthetic"])
+        eng_mod = __import__("needle_cs_b200.engine", fromlist=["engine"])
+        model = eng_mod.SyntheticDecoder(seed=1)
+        threads = threads or os.cpu_count() or 1
+        layers, fnorm, emb, wh, sh = syn.decoder_weights(model)
+        dec = oracle.Decoder(model, layers, fnorm, emb, wh, sh, 512)
+        n = max(1, min(threads, 16))
+        kvs = [dec.new_kv() for _ in range(n)]
+        depth = 24  # positions per sampled request
+
+        def one(j):
+            for pos in range(depth):
+                dec.row(int(prompts[j][pos % len(prompts[j])]), pos, kvs[j])
+
+        t0 = time.perf_counter()
+        with ThreadPoolExecutor(max_workers=threads) as pool:
+            list(pool.map(one, range(n)))
+        rows_per_s = n * depth / (time.perf_counter() - t0)
+        total_rows = sum(len(p) for p in prompts) + sum(outs)
+        value = sum(outs) / (total_rows / rows_per_s)
+        return value, threads, (f"{n} requests x {depth} positions through the scalar C restatement "
+                                f"({rows_per_s:.0f} rows/s on {threads} threads); the trace's "
+                                f"{total_rows} rows at that rate")
+
+
+def run_serving(args, rank, world, local):
+    import torch
+
+    entry.load_package().lib()
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    wl = ServingWorkload()
+    wl.setup(device, rank, world)
+    # warm-up trace (separate request ids), then the measured trace
+    wa, wp, wo, wm = wl.trace(rank, n=16, seed=wl.seed + 100)
+    wl.serve(wa * 0, wp, [min(o, 8) for o in wo], wm, id_base=1_000_000)
+    arrivals, prompts, outs, masks = wl.trace(rank)
+    barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(torch.cuda.get_device_properties(device).uuid) as clocks:
+        r = wl.serve(arrivals, prompts, outs, masks)
+    torch.cuda.synchronize()
+    barrier(world)
+    makespan = max_over_ranks(r["makespan_s"] * 1e3, world) * 1e-3
+    value = world * r["out_tokens"] / makespan
+    ttft = r["ttft_ms"]
+    line = {"metric": "serving output tokens/sec/box", "value": value, "unit": "tokens/s", "n_gpus": world,
+            "steps": r["steps"], "warmup": 1, "ms_per_step": makespan * 1e3 / max(r["steps"], 1),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8xint8->int32,f32",
+            "data": "synthetic", "config": wl.describe(),
+            "ttft_ms": {"mean": float(ttft.mean()), "p50": float(np.percentile(ttft, 50)),
+                        "p99": float(np.percentile(ttft, 99))},
+            "goodput_requests_per_s": world * r["good"] / makespan, "failed_requests": r["failed"],
+            "rows_per_step": r["rows"] / max(r["steps"], 1), "decode_rows": r["decode_rows"],
+            "prefill_rows": r["rows"] - r["decode_rows"], "makespan_s": makespan,
+            "roofline": None,
+            "e2e": {"value": value, "unit": "tokens/s",
+                    "h2d_bytes_per_step": 4 * r["rows"] * 3 // max(r["steps"], 1),
+                    "d2h_bytes_per_step": 4 * (r["decode_rows"] + 1) // max(r["steps"], 1)},
+            "gpu_launches": r["steps"] * (1 + 12 * 10 + 3 + 1),
+            "clocks": clocks.summary()}
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        oracle = entry.load_oracle()
+        v, cores, sample = wl.cpu_sample(oracle, arrivals, prompts, outs)
+        line["cpu_baseline"] = {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    wl.engine.close()
+
+
+WORKLOADS = {"cfg1": GemvWorkload, "cfg2": DecodeWorkload, "cfg3": ServingWorkload, "cfg5": DecodeWorkload}
 DECODE = ("cfg2", "cfg5")
 
 
@@ -354,7 +513,11 @@ def run_reference(args, rank, world):
     wl = make_workload(args.workload, args)
     wl.ops = __import__("needle_cs_b200.ops", fromlist=["ops"])
     per_step = []
-    if args.workload in DECODE:
+    if args.workload == "cfg3":
+        arrivals, prompts, outs, _ = wl.trace(0)
+        value, cores, sample = wl.cpu_sample(oracle, arrivals, prompts, outs)
+        metric, unit = "serving output tokens/sec/box", "tokens/s"
+    elif args.workload in DECODE:
         for i in range(max(1, args.steps // 10)):
             v, cores, sample = wl.cpu_sample(oracle)
             per_step.append(v)
@@ -554,6 +717,8 @@ def main():
     try:
         if args.workload in DECODE:
             run_decode(args, rank, world, local)
+        elif args.workload == "cfg3":
+            run_serving(args, rank, world, local)
         else:
             run_ours(args, rank, world, local)
     finally:
