@@ -191,11 +191,16 @@ typedef struct ndl_engine ndl_engine;
 /* Synthetic decoder (I8G32 weights generated on the device from `seed`):
  * RMSNorm -> int8 QKV -> RoPE -> paged int8 KV -> attention -> int8 O ->
  * residual; RMSNorm -> int8 gate|up -> SwiGLU -> int8 down -> residual;
- * final RMSNorm -> int8 head quantized from the fp16 embedding. */
+ * final RMSNorm -> int8 head quantized from the fp16 embedding.  With
+ * `cross`, each layer adds after its self-attention residual
+ * x += W_co . Attn(W_cq . RMSNorm(x), memory) over the memory attached to
+ * the row's slot (the reference's cross branch, src/Needle/Engine.cs:
+ * 1098-1184, with the synthetic decoder's int8 linears). */
 typedef struct {
     int layers, dim, heads, head_dim, ffn, vocab;
     float rope_theta; /* <= 0 selects 10000 */
     uint64_t seed;
+    int cross; /* 1: every layer has a cross-attention block (Whistle-shaped decoder) */
 } ndl_decoder_config;
 
 typedef struct {
@@ -243,6 +248,7 @@ enum {
     NDL_PROF_GEMM_DOWN,
     NDL_PROF_HEAD,
     NDL_PROF_SAMPLE,
+    NDL_PROF_CROSS, /* the cross-attention blocks */
     NDL_PROF_CLASSES
 };
 NDL_API int ndl_engine_profile(ndl_engine *e, int enable);
@@ -262,6 +268,43 @@ NDL_API int ndl_slot_page(ndl_engine *e, int slot, int index, int *page);
 /* Appends `count` synthetic prefix positions to a slot: K/V fp16 N(0,1)
  * from (seed, session) quantized per (position, head) on load. */
 NDL_API int ndl_slot_fill_synthetic(ndl_engine *e, int slot, int count, uint64_t seed, uint64_t session);
+
+/* Cross memory (Whistle-shaped decoders).  A memory slot holds one
+ * utterance's encoder output projected per layer into int8 K/V pages
+ * (BuildCrossMemory + per-(frame, head) quantize, src/Needle/Whistle.cs:
+ * 886-914,789-790: every frame row quantized, W_ckv [2*dim][dim], each
+ * head's 64 K and V values QuantizeInt8).  set_memory takes the fp16
+ * [frames][dim] memory from the host; fill_memory_synthetic generates it as
+ * fp16 N(0,1) from (seed, utterance) on the device.  The slot must be empty;
+ * its length becomes `frames`.  attach_memory makes the rows of `slot` attend
+ * to `memory_slot` (-1 detaches); beams of one utterance share it. */
+NDL_API int ndl_slot_set_memory(ndl_engine *e, int slot, const uint16_t *memory, int frames);
+NDL_API int ndl_slot_fill_memory_synthetic(ndl_engine *e, int slot, int frames, uint64_t seed, uint64_t utterance);
+NDL_API int ndl_slot_attach_memory(ndl_engine *e, int slot, int memory_slot);
+/* Copies slot `src` (its positions, pages and memory attachment) into `dst`,
+ * replacing dst's content: the beam fork of Engine.CopyFrom
+ * (src/Needle/Engine.cs:367-379). */
+NDL_API int ndl_slot_copy(ndl_engine *e, int dst, int src);
+
+/* Beam search over many utterances at once: Whistle.BeamSearch
+ * (src/Needle/Whistle.Decode.cs:224-350) for each utterance, every live
+ * beam of every utterance in one forward_batch per step.  Utterance u uses
+ * memory slot memory_slots[u] and the 2*width beam slots
+ * beam_slots[u*2*width ...] (reset here).  Each beam starts from `prompt`;
+ * per step the top-width of every beam's log-softmax (ids 0, 2, 3 excluded
+ * when mask_special_023) extend it; candidates are ranked by score (equal
+ * scores keep (beam, rank) order), eos ends a hypothesis; the search stops
+ * when no beam stays live, when width hypotheses finished and the best
+ * finished score/(len+1)^length_penalty beats the best live one, or after
+ * max_steps.  tokens [utterances][max_steps], lengths, scores (normalised,
+ * nullable) receive each utterance's winner. */
+typedef struct {
+    int width, max_steps, eos, mask_special_023;
+    float length_penalty;
+} ndl_beam_config;
+NDL_API int ndl_beam_search(ndl_engine *e, const ndl_beam_config *cfg, int utterances, const int *memory_slots,
+                            const int *beam_slots, const int32_t *prompt, int prompt_len, int32_t *tokens,
+                            int *lengths, float *scores);
 
 /* One batched step: EngineCore.ForwardBatch (src/Needle/Engine.cs:2303-2350)
  * via BatchedEngine.ForwardBatch (src/Needle/BatchEngine.cs:34).  Host

@@ -61,6 +61,12 @@ SIGNATURES = {
     "ndl_engine_set_mask": (c_int, [c_void_p, c_int, c_void_p, c_int]),
     "ndl_sample_argmax_slots": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p]),
     "ndl_engine_get_info": (c_int, [c_void_p, c_void_p]),
+    "ndl_slot_set_memory": (c_int, [c_void_p, c_int, c_void_p, c_int]),
+    "ndl_slot_fill_memory_synthetic": (c_int, [c_void_p, c_int, c_int, c_u64, c_u64]),
+    "ndl_slot_attach_memory": (c_int, [c_void_p, c_int, c_int]),
+    "ndl_slot_copy": (c_int, [c_void_p, c_int, c_int]),
+    "ndl_beam_search": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_void_p,
+                                c_void_p]),
     "ndl_sched_create": (c_int, [c_void_p, c_void_p, c_void_p]),
     "ndl_sched_create_dry": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p]),
     "ndl_sched_destroy": (c_int, [c_void_p]),
@@ -75,19 +81,25 @@ SIGNATURES = {
 }
 
 PROF_CLASSES = ["prepare", "norm_quant", "gemm_qkv", "kv_write", "attention", "gemm_o", "gemm_gateup", "swiglu",
-                "gemm_down", "head", "sample"]
+                "gemm_down", "head", "sample", "cross"]
 
 
 class DecoderConfig(ctypes.Structure):
     """ndl_decoder_config."""
     _fields_ = [("layers", c_int), ("dim", c_int), ("heads", c_int), ("head_dim", c_int), ("ffn", c_int),
-                ("vocab", c_int), ("rope_theta", c_float), ("seed", c_u64)]
+                ("vocab", c_int), ("rope_theta", c_float), ("seed", c_u64), ("cross", c_int)]
 
 
 class EngineInfo(ctypes.Structure):
     """ndl_engine_info."""
     _fields_ = [("slots", c_int), ("capacity", c_int), ("vocab", c_int), ("max_rows", c_int), ("max_heads", c_int),
                 ("layers", c_int), ("dim", c_int), ("heads", c_int)]
+
+
+class BeamConfig(ctypes.Structure):
+    """ndl_beam_config."""
+    _fields_ = [("width", c_int), ("max_steps", c_int), ("eos", c_int), ("mask_special_023", c_int),
+                ("length_penalty", c_float)]
 
 
 class SchedConfig(ctypes.Structure):

@@ -113,6 +113,70 @@ int launch_kv_write(const KvWriteArgs &a, cudaStream_t stream) {
     return check_launch("kv_write");
 }
 
+// ------------------------------------------------------- cross attention --
+// Queries of the cross-attention block: per (row, head) quantize (no RoPE:
+// the memory has no positions) into q8 in k_slot order.  Warp per (row, head).
+__global__ void __launch_bounds__(256) cross_query_kernel(const float *__restrict__ q, int ldq, int heads, int rows,
+                                                          int8_t *__restrict__ q8, float *__restrict__ qs) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (warp >= rows * heads) return;
+    const int row = warp / heads, head = warp - row * heads;
+    const float *src = q + (size_t)row * ldq + head * kHeadDim;
+    int8_t lo8, hi8;
+    const float scale = warp_quantize64(src[lane], src[lane + 32], lo8, hi8);
+    int8_t *qo = q8 + ((size_t)row * heads + head) * kHeadDim;
+    qo[k_slot(lane)] = lo8;
+    qo[k_slot(lane + 32)] = hi8;
+    if (lane == 0) qs[(size_t)row * heads + head] = scale;
+}
+
+int launch_cross_query(const float *q, int ldq, int heads, int rows, int8_t *q8, float *qs, cudaStream_t stream) {
+    const int warps = rows * heads;
+    if (warps == 0) return NDL_OK;
+    cross_query_kernel<<<(warps + 7) / 8, 256, 0, stream>>>(q, ldq, heads, rows, q8, qs);
+    return check_launch("cross_query");
+}
+
+// Cross memory of one layer into the pages of a memory slot: y [frames][2*dim]
+// holds the projected K | V of every frame; per (frame, head) the 64 K and 64
+// V values are quantized (QuantizeInt8, src/Needle/Whistle.cs:789-790) and
+// stored at the frame's position like self-attention keys.  Warp per
+// (frame, head); page_row = the slot's page-table row.
+__global__ void __launch_bounds__(256) cross_kv_write_kernel(const float *__restrict__ y, int frames, int heads,
+                                                             const int32_t *__restrict__ page_row, int num_pages,
+                                                             uint8_t *__restrict__ pool, long long page_bytes,
+                                                             int layer, int *status) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (warp >= frames * heads) return;
+    const int f = warp / heads, head = warp - f * heads;
+    const int dim = heads * kHeadDim;
+    const int page = page_row[f / kPagePositions], j = f % kPagePositions;
+    if (page < 0 || page >= num_pages) {
+        if (lane == 0 && status) atomicOr(status, kStatusBadPage);
+        return;
+    }
+    uint8_t *blk = pool + (size_t)page * page_bytes + kv_block_offset(layer, head, heads);
+    const float *kr = y + (size_t)f * 2 * dim + head * kHeadDim, *vr = kr + dim;
+    int8_t lo8, hi8;
+    float scale = warp_quantize64(kr[lane], kr[lane + 32], lo8, hi8);
+    blk[k_byte(j, lane)] = (uint8_t)lo8;
+    blk[k_byte(j, lane + 32)] = (uint8_t)hi8;
+    if (lane == 0) reinterpret_cast<float *>(blk + kKScaleOffset)[scale_slot(j)] = scale;
+    scale = warp_quantize64(vr[lane], vr[lane + 32], lo8, hi8);
+    blk[v_byte(j, lane)] = (uint8_t)lo8;
+    blk[v_byte(j, lane + 32)] = (uint8_t)hi8;
+    if (lane == 0) reinterpret_cast<float *>(blk + kVScaleOffset)[scale_slot(j)] = scale;
+}
+
+int launch_cross_kv_write(const float *y, int frames, int heads, const int32_t *page_row, int num_pages, uint8_t *pool,
+                          long long page_bytes, int layer, int *status, cudaStream_t stream) {
+    const long long warps = (long long)frames * heads;
+    if (warps == 0) return NDL_OK;
+    cross_kv_write_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, stream>>>(y, frames, heads, page_row, num_pages,
+                                                                           pool, page_bytes, layer, status);
+    return check_launch("cross_kv_write");
+}
+
 // ------------------------------------------------------ decode attention --
 constexpr int kAttnWarps = 4;
 constexpr int kAttnStages = 2;

@@ -35,13 +35,18 @@ int launch_topk_logsoftmax(const float *x, long long ldx, int n, int k, int mask
                            float *logp, float *probs, cudaStream_t stream);
 int launch_kv_fill(uint64_t seed, uint64_t session, int layers, int heads, int first, int count,
                    const int32_t *page_row, uint8_t *pool, long long page_bytes, cudaStream_t stream);
+int launch_half_to_float(const uint16_t *src, long long n, float *dst, cudaStream_t stream);
 
 // Stream ids of the synthetic decoder tensors under the model seed.
 enum : uint64_t {
     kStreamEmbedding = 1,
     kStreamFinalNorm = 2,
-    kStreamLayerBase = 100,  // + 16 * layer + field
+    kStreamLayerBase = 100,   // + 16 * layer + field
+    kStreamCrossBase = 5000,  // + 16 * layer + cross field
 };
+enum : int { kFCqW, kFCqS, kFCkvW, kFCkvS, kFCoW, kFCoS, kFCrossNorm };
+// fp16 N(0,1) encoder memory of an utterance: stream kStreamMemory + utterance
+constexpr uint64_t kStreamMemory = 1ull << 40;
 constexpr int kAttnChunkPages = 8;  // pages per attention work item (512 positions)
 enum : int { kFQkvW, kFQkvS, kFOW, kFOS, kFGuW, kFGuS, kFDW, kFDS, kFAttnNorm, kFFfnNorm };
 
@@ -49,6 +54,10 @@ struct DeviceLayer {
     int8_t *w_qkv, *w_o, *w_gu, *w_d;
     uint16_t *s_qkv, *s_o, *s_gu, *s_d;
     float *attn_norm, *ffn_norm;
+    // cross-attention block (decoders with `cross`)
+    int8_t *w_cq = nullptr, *w_ckv = nullptr, *w_co = nullptr;
+    uint16_t *s_cq = nullptr, *s_ckv = nullptr, *s_co = nullptr;
+    float *cross_norm = nullptr;
 };
 
 }  // namespace ndl
@@ -73,6 +82,7 @@ struct ndl_engine {
     std::vector<int32_t> page_table;  // host mirror [slots][max_pages]
     std::vector<int32_t> free_pages;
     std::vector<int> slot_len, slot_mark;
+    std::vector<int> cross_slot;  // memory slot attended by each slot's rows (-1: none)
     // step buffers
     float *x = nullptr, *qkv = nullptr, *attn = nullptr, *gu = nullptr, *act = nullptr, *head_x = nullptr;
     int8_t *qa = nullptr, *q8 = nullptr;
@@ -112,7 +122,8 @@ struct ndl_engine {
     double prof_ms[NDL_PROF_CLASSES] = {0};
     long long prof_count[NDL_PROF_CLASSES] = {0};
     // offsets of the last step's metadata in d_meta
-    int off_tokens = 0, off_slot = 0, off_pos = 0, off_order = 0, off_head = 0, off_updates = 0;
+    int off_tokens = 0, off_slot = 0, off_pos = 0, off_order = 0, off_cslot = 0, off_cpos = 0, off_head = 0,
+        off_updates = 0;
 };
 
 using namespace ndl;
@@ -214,6 +225,24 @@ int build_weights(ndl_engine *e) {
         TRY(upload(e, L.attn_norm, host.data(), d * sizeof(float)));
         norm_values(seed, layer_stream(l, kFFfnNorm), d, host);
         TRY(upload(e, L.ffn_norm, host.data(), d * sizeof(float)));
+        if (c.cross) {
+            auto cs = [&](int f) { return (uint64_t)kStreamCrossBase + 16ull * l + (uint64_t)f; };
+            TRY(dalloc(e, &L.w_cq, (size_t)d * d));
+            TRY(dalloc(e, &L.s_cq, (size_t)d * G));
+            TRY(dalloc(e, &L.w_ckv, (size_t)2 * d * d));
+            TRY(dalloc(e, &L.s_ckv, (size_t)2 * d * G));
+            TRY(dalloc(e, &L.w_co, (size_t)d * d));
+            TRY(dalloc(e, &L.s_co, (size_t)d * G));
+            TRY(dalloc(e, &L.cross_norm, d));
+            TRY(ndl_synth_int8_device(seed, cs(kFCqW), 0, (size_t)d * d, L.w_cq, s));
+            TRY(ndl_synth_uniform_f16_device(seed, cs(kFCqS), 0, (size_t)d * G, 0.001f, 0.02f, L.s_cq, s));
+            TRY(ndl_synth_int8_device(seed, cs(kFCkvW), 0, (size_t)2 * d * d, L.w_ckv, s));
+            TRY(ndl_synth_uniform_f16_device(seed, cs(kFCkvS), 0, (size_t)2 * d * G, 0.001f, 0.02f, L.s_ckv, s));
+            TRY(ndl_synth_int8_device(seed, cs(kFCoW), 0, (size_t)d * d, L.w_co, s));
+            TRY(ndl_synth_uniform_f16_device(seed, cs(kFCoS), 0, (size_t)d * G, 0.001f, 0.02f, L.s_co, s));
+            norm_values(seed, cs(kFCrossNorm), d, host);
+            TRY(upload(e, L.cross_norm, host.data(), d * sizeof(float)));
+        }
     }
     TRY(dalloc(e, &e->final_norm, d));
     norm_values(seed, kStreamFinalNorm, d, host);
@@ -268,8 +297,9 @@ int build_buffers(ndl_engine *e) {
     NDL_CUDA(cudaMemsetAsync(e->arrivals, 0, (size_t)R * c.heads * sizeof(int), e->stream));
     TRY(dalloc(e, &e->d_status, 1));
     NDL_CUDA(cudaMemsetAsync(e->d_status, 0, sizeof(int), e->stream));
-    // metadata: tokens, slots, positions, order (R each) + head rows (Hd) + updates (3 per row + slack)
-    e->meta_ints = (size_t)4 * R + Hd + 3 * (size_t)R + 64;
+    // metadata: tokens, slots, positions, order, memory slot, memory position
+    // (R each) + head rows (Hd) + updates (3 per row + slack)
+    e->meta_ints = (size_t)6 * R + Hd + 3 * (size_t)R + 64;
     TRY(dalloc(e, &e->d_meta, e->meta_ints));
     NDL_CUDA(cudaMallocHost(&e->h_meta, e->meta_ints * sizeof(int32_t)));
     TRY(dalloc(e, &e->d_ids, (size_t)Hd * 8));
@@ -401,6 +431,21 @@ int step_kernels(ndl_engine *e, int rows, int heads) {
             ProfScope p(e, NDL_PROF_GEMM_O);
             TRY(ndl_matmul_i8g32(e->qa, e->sa, rows, L.w_o, L.s_o, d, d, e->x, d, e->x, nullptr, s));
         }
+        if (c.cross) {
+            // x += W_co . Attn(W_cq . RMSNorm(x), memory of the row's slot)
+            ProfScope p(e, NDL_PROF_CROSS);
+            const int32_t *d_cslot = e->d_meta + e->off_cslot, *d_cpos = e->d_meta + e->off_cpos;
+            TRY(launch_quantize_rows(e->x, L.cross_norm, rows, d, e->qa, e->sa, s));
+            TRY(ndl_matmul_i8g32(e->qa, e->sa, rows, L.w_cq, L.s_cq, d, d, e->qkv, d, nullptr, nullptr, s));
+            TRY(launch_cross_query(e->qkv, d, c.heads, rows, e->q8, e->qs, s));
+            AttnArgs ca{e->q8, e->qs, d_cslot, d_cpos, d_order, e->d_page_table, e->max_pages, e->pool,
+                        (long long)e->page_bytes, e->ec.kv_pages, l, c.heads, rows, chunk_pages, max_chunks,
+                        1.0f / sqrtf((float)c.head_dim), e->attn, e->partials, e->arrivals, e->d_status,
+                        e->ec.slots};
+            TRY(launch_attn_decode(ca, s));
+            TRY(launch_quantize_rows(e->attn, nullptr, rows, d, e->qa, e->sa, s));
+            TRY(ndl_matmul_i8g32(e->qa, e->sa, rows, L.w_co, L.s_co, d, d, e->x, d, e->x, nullptr, s));
+        }
         {
             ProfScope p(e, NDL_PROF_NORM_QUANT);
             TRY(launch_quantize_rows(e->x, L.ffn_norm, rows, d, e->qa, e->sa, s));
@@ -512,6 +557,7 @@ NDL_API int ndl_engine_create(const ndl_engine_config *ec, const ndl_decoder_con
     for (int i = 0; i < pages; i++) e->free_pages[i] = pages - 1 - i;  // pop_back yields 0, 1, 2, ...
     e->slot_len.assign(ec->slots, 0);
     e->slot_mark.assign(ec->slots, 0);
+    e->cross_slot.assign(ec->slots, -1);
     *out = e;
     return NDL_OK;
 }
@@ -553,6 +599,13 @@ NDL_API int ndl_engine_tensor(ndl_engine *e, const char *name, int layer, void *
         else if (n == "s_d") { *ptr = L.s_d; *bytes = d * GF * 2; }
         else if (n == "attn_norm") { *ptr = L.attn_norm; *bytes = d * 4; }
         else if (n == "ffn_norm") { *ptr = L.ffn_norm; *bytes = d * 4; }
+        else if (c.cross && n == "w_cq") { *ptr = L.w_cq; *bytes = d * d; }
+        else if (c.cross && n == "s_cq") { *ptr = L.s_cq; *bytes = d * G * 2; }
+        else if (c.cross && n == "w_ckv") { *ptr = L.w_ckv; *bytes = 2 * d * d; }
+        else if (c.cross && n == "s_ckv") { *ptr = L.s_ckv; *bytes = 2 * d * G * 2; }
+        else if (c.cross && n == "w_co") { *ptr = L.w_co; *bytes = d * d; }
+        else if (c.cross && n == "s_co") { *ptr = L.s_co; *bytes = d * G * 2; }
+        else if (c.cross && n == "cross_norm") { *ptr = L.cross_norm; *bytes = d * 4; }
         else return set_error(NDL_ERR_INVALID_ARG, "unknown layer tensor '%s'", name);
         return NDL_OK;
     }
@@ -655,6 +708,134 @@ NDL_API int ndl_slot_fill_synthetic(ndl_engine *e, int slot, int count, uint64_t
     return NDL_OK;
 }
 
+namespace {
+
+// Pages for positions [first, first + count) of a slot (host mirror + device table).
+int reserve_pages(ndl_engine *e, int slot, int first, int count) {
+    std::vector<int32_t> updates;
+    int32_t *row = e->page_table.data() + (size_t)slot * e->max_pages;
+    for (int p = first / kPagePositions; p * kPagePositions < first + count; p++) {
+        if (row[p] < 0) {
+            if (e->free_pages.empty()) return set_error(NDL_ERR_PAGES_EXHAUSTED, "KV page pool exhausted");
+            row[p] = e->free_pages.back();
+            e->free_pages.pop_back();
+            updates.insert(updates.end(), {slot, p, row[p]});
+        }
+    }
+    return push_page_updates(e, updates);
+}
+
+// Builds the memory K/V of every layer from fp16 memory already on the device.
+int build_memory(ndl_engine *e, int slot, const uint16_t *d_mem16, int frames) {
+    const int d = e->dc.dim;
+    cudaStream_t s = e->stream;
+    TRY(reserve_pages(e, slot, 0, frames));
+    float *mem = nullptr, *y = nullptr, *sa = nullptr;
+    int8_t *q = nullptr;
+    int st = NDL_OK;
+    auto cleanup = [&]() {
+        cudaStreamSynchronize(s);
+        cudaFree(mem);
+        cudaFree(y);
+        cudaFree(sa);
+        cudaFree(q);
+    };
+    if (cudaMalloc(&mem, (size_t)frames * d * 4) != cudaSuccess || cudaMalloc(&y, (size_t)frames * 2 * d * 4) != cudaSuccess ||
+        cudaMalloc(&sa, (size_t)frames * 4) != cudaSuccess || cudaMalloc(&q, (size_t)frames * d) != cudaSuccess) {
+        cudaGetLastError();
+        cleanup();
+        return set_error(NDL_ERR_OUT_OF_MEMORY, "cross memory scratch (%d frames)", frames);
+    }
+    st = launch_half_to_float(d_mem16, (long long)frames * d, mem, s);
+    if (st == NDL_OK) st = launch_quantize_rows(mem, nullptr, frames, d, q, sa, s);
+    for (int l = 0; l < e->dc.layers && st == NDL_OK; l++) {
+        const DeviceLayer &L = e->layers[l];
+        st = ndl_matmul_i8g32(q, sa, frames, L.w_ckv, L.s_ckv, 2 * d, d, y, 2 * d, nullptr, nullptr, s);
+        if (st == NDL_OK)
+            st = launch_cross_kv_write(y, frames, e->dc.heads, e->d_page_table + (size_t)slot * e->max_pages,
+                                       e->ec.kv_pages, e->pool, (long long)e->page_bytes, l, e->d_status, s);
+    }
+    cleanup();
+    if (st != NDL_OK) return st;
+    TRY(check_status(e));
+    e->slot_len[slot] = frames;
+    return NDL_OK;
+}
+
+int check_memory_slot(ndl_engine *e, int slot, int frames) {
+    TRY(check_slot(e, slot));
+    NDL_REQUIRE(e->dc.cross, "the decoder has no cross-attention blocks");
+    NDL_REQUIRE(e->slot_len[slot] == 0, "memory slot %d is not empty", slot);
+    NDL_REQUIRE(frames >= 1 && frames <= e->ec.capacity, "frames %d outside 1..%d", frames, e->ec.capacity);
+    return NDL_OK;
+}
+
+}  // namespace
+
+NDL_API int ndl_slot_set_memory(ndl_engine *e, int slot, const uint16_t *memory, int frames) {
+    NDL_REQUIRE(e && memory, "null argument");
+    TRY(check_memory_slot(e, slot, frames));
+    const size_t bytes = (size_t)frames * e->dc.dim * 2;
+    uint16_t *d_mem = nullptr;
+    if (cudaMalloc(&d_mem, bytes) != cudaSuccess) {
+        cudaGetLastError();
+        return set_error(NDL_ERR_OUT_OF_MEMORY, "cross memory upload (%zu bytes)", bytes);
+    }
+    int st = cudaMemcpyAsync(d_mem, memory, bytes, cudaMemcpyHostToDevice, e->stream) == cudaSuccess
+                 ? build_memory(e, slot, d_mem, frames)
+                 : set_error(NDL_ERR_CUDA, "cross memory upload failed");
+    cudaStreamSynchronize(e->stream);
+    cudaFree(d_mem);
+    return st;
+}
+
+NDL_API int ndl_slot_fill_memory_synthetic(ndl_engine *e, int slot, int frames, uint64_t seed, uint64_t utterance) {
+    NDL_REQUIRE(e, "null engine");
+    TRY(check_memory_slot(e, slot, frames));
+    const size_t count = (size_t)frames * e->dc.dim;
+    uint16_t *d_mem = nullptr;
+    if (cudaMalloc(&d_mem, count * 2) != cudaSuccess) {
+        cudaGetLastError();
+        return set_error(NDL_ERR_OUT_OF_MEMORY, "cross memory (%zu values)", count);
+    }
+    int st = ndl_synth_normal_f16_device(seed, kStreamMemory + utterance, 0, count, 1.0f, d_mem, e->stream);
+    if (st == NDL_OK) st = build_memory(e, slot, d_mem, frames);
+    cudaStreamSynchronize(e->stream);
+    cudaFree(d_mem);
+    return st;
+}
+
+NDL_API int ndl_slot_attach_memory(ndl_engine *e, int slot, int memory_slot) {
+    NDL_REQUIRE(e, "null engine");
+    TRY(check_slot(e, slot));
+    NDL_REQUIRE(e->dc.cross, "the decoder has no cross-attention blocks");
+    NDL_REQUIRE(memory_slot >= -1 && memory_slot < e->ec.slots && memory_slot != slot, "memory slot %d",
+                memory_slot);
+    e->cross_slot[slot] = memory_slot;
+    return NDL_OK;
+}
+
+NDL_API int ndl_slot_copy(ndl_engine *e, int dst, int src) {
+    NDL_REQUIRE(e, "null engine");
+    TRY(check_slot(e, dst));
+    TRY(check_slot(e, src));
+    if (dst == src) return NDL_OK;
+    std::vector<int32_t> updates;
+    free_slot_pages(e, dst, 0, &updates);
+    TRY(push_page_updates(e, updates));
+    const int len = e->slot_len[src];
+    TRY(reserve_pages(e, dst, 0, len));
+    const int32_t *rs = e->page_table.data() + (size_t)src * e->max_pages;
+    const int32_t *rd = e->page_table.data() + (size_t)dst * e->max_pages;
+    for (int p = 0; p * kPagePositions < len; p++)
+        NDL_CUDA(cudaMemcpyAsync(e->pool + (size_t)rd[p] * e->page_bytes, e->pool + (size_t)rs[p] * e->page_bytes,
+                                 e->page_bytes, cudaMemcpyDeviceToDevice, e->stream));
+    e->slot_len[dst] = len;
+    e->slot_mark[dst] = e->slot_mark[src];
+    e->cross_slot[dst] = e->cross_slot[src];
+    return NDL_OK;
+}
+
 // EngineCore.ForwardBatch (src/Needle/Engine.cs:2303-2350).
 NDL_API int ndl_forward_batch(ndl_engine *e, const int *tokens, const int *row_slots, int rows, const int *head_rows,
                               int heads) {
@@ -666,8 +847,9 @@ NDL_API int ndl_forward_batch(ndl_engine *e, const int *tokens, const int *row_s
     // positions, capacity check, page allocation (host)
     int32_t *m = e->h_meta;
     const int R = e->ec.max_rows;
-    e->off_tokens = 0, e->off_slot = R, e->off_pos = 2 * R, e->off_order = 3 * R, e->off_head = 4 * R;
-    e->off_updates = 4 * R + e->ec.max_heads;
+    e->off_tokens = 0, e->off_slot = R, e->off_pos = 2 * R, e->off_order = 3 * R, e->off_cslot = 4 * R,
+    e->off_cpos = 5 * R, e->off_head = 6 * R;
+    e->off_updates = 6 * R + e->ec.max_heads;
     std::vector<int> advance;
     advance.reserve(rows);
     int max_len = 0;
@@ -685,6 +867,13 @@ NDL_API int ndl_forward_batch(ndl_engine *e, const int *tokens, const int *row_s
         m[e->off_tokens + r] = tokens[r];
         m[e->off_slot + r] = slot;
         m[e->off_pos + r] = pos;
+        if (c.cross) {
+            const int ms = e->cross_slot[slot];
+            if (ms < 0 || e->slot_len[ms] < 1)
+                return set_error(NDL_ERR_INVALID_ARG, "slot %d has no cross memory attached", slot);
+            m[e->off_cslot + r] = ms;
+            m[e->off_cpos + r] = e->slot_len[ms] - 1;
+        }
         max_len = std::max(max_len, pos + 1);
     }
     for (int h = 0; h < heads; h++) {

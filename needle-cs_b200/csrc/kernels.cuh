@@ -45,6 +45,11 @@ struct KvWriteArgs {
     int *status;
 };
 int launch_kv_write(const KvWriteArgs &a, cudaStream_t stream);
+// Cross-attention queries (per-head quantize, no RoPE) and the memory K/V of
+// one layer written into a memory slot's pages.
+int launch_cross_query(const float *q, int ldq, int heads, int rows, int8_t *q8, float *qs, cudaStream_t stream);
+int launch_cross_kv_write(const float *y, int frames, int heads, const int32_t *page_row, int num_pages, uint8_t *pool,
+                          long long page_bytes, int layer, int *status, cudaStream_t stream);
 
 constexpr int kPartialFloats = 68;  // 64 outputs + peak + sum, padded to 16 bytes
 

@@ -1,6 +1,8 @@
 // Small kernels of the batched decode step: step preparation (page-table
 // updates + embedding gather), SwiGLU + quantize, head-row gather, masked
 // argmax with probability, top-k log-softmax, and the synthetic KV fill.
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.cuh"
 #include "kv.cuh"
@@ -312,6 +314,20 @@ int launch_kv_fill(uint64_t seed, uint64_t session, int layers, int heads, int f
     kv_fill_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, stream>>>(synth_key(seed, session), layers, heads, first,
                                                                      count, page_row, pool, page_bytes);
     return check_launch("kv_fill");
+}
+
+// fp16 bits -> fp32 (the reference's HalfToSingle, exact), e.g. the encoder
+// memory before its rows are quantized.
+__global__ void half_to_float_kernel(const uint16_t *__restrict__ src, long long n, float *__restrict__ dst) {
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+        dst[i] = half_to_float_ref(src[i]);
+}
+
+int launch_half_to_float(const uint16_t *src, long long n, float *dst, cudaStream_t stream) {
+    if (n <= 0) return NDL_OK;
+    const long long blocks = std::min<long long>((n + 255) / 256, 148 * 16);
+    half_to_float_kernel<<<(unsigned)blocks, 256, 0, stream>>>(src, n, dst);
+    return check_launch("half_to_float");
 }
 
 }  // namespace ndl

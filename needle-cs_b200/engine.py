@@ -26,10 +26,17 @@ class SyntheticDecoder:
     vocab: int = 8192
     rope_theta: float = 10000.0
     seed: int = 1
+    cross: int = 0  # 1: a cross-attention block per layer (Whistle-shaped decoder)
 
     def native(self):
         return DecoderConfig(self.layers, self.dim, self.heads, self.head_dim, self.ffn, self.vocab, self.rope_theta,
-                             self.seed)
+                             self.seed, int(self.cross))
+
+
+def whistle_decoder(seed=3):
+    """The cfg4 decoder: 4 layers, d 384, 6x64 heads, SwiGLU 1536, vocab 51865,
+    cross-attention to a per-utterance encoder memory."""
+    return SyntheticDecoder(layers=4, dim=384, heads=6, head_dim=64, ffn=1536, vocab=51865, seed=seed, cross=1)
 
 
 def _i32(a):
@@ -142,6 +149,22 @@ class BatchedEngine:
         else:
             call("ndl_sample_argmax", self._h, None, 0, ids.ctypes.data, probs.ctypes.data if with_probs else None)
         return (ids, probs) if with_probs else ids
+
+    # -- cross memory (Whistle-shaped decoders) --
+    def set_memory(self, slot, memory_f16_bits):
+        """Projects fp16 memory [frames][dim] (uint16 bits) into the K/V pages of an empty slot."""
+        m = np.ascontiguousarray(memory_f16_bits, dtype=np.uint16)
+        call("ndl_slot_set_memory", self._h, slot, m.ctypes.data, m.shape[0])
+
+    def fill_memory_synthetic(self, slot, frames, seed, utterance):
+        call("ndl_slot_fill_memory_synthetic", self._h, slot, frames, seed, utterance)
+
+    def attach_memory(self, slot, memory_slot):
+        call("ndl_slot_attach_memory", self._h, slot, memory_slot)
+
+    def copy_slot(self, dst, src):
+        """Engine.CopyFrom (Engine.cs:367-379): dst becomes a copy of src."""
+        call("ndl_slot_copy", self._h, dst, src)
 
     def set_mask(self, slot, mask=None):
         """Keeps a vocabulary bitmask for `slot` on the device (None clears it)."""

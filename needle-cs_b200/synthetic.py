@@ -10,12 +10,18 @@ at 100 + 16*l + f with f = 0 w_qkv, 1 s_qkv, 2 w_o, 3 s_o, 4 w_gu, 5 s_gu,
 scales fp16 U(0.001, 0.02), norms 1 + 0.1*normal (fp32), the embedding fp16
 0.02*normal, and the head int8 quantized from the embedding per
 (row, 32-group) with s = fp16(max|e|/127), w = clamp(rint(e/float(s)), +-127).
+Cross-attention blocks (decoders with `cross`): layer l field f at
+5000 + 16*l + f with f = 0 w_cq, 1 s_cq, 2 w_ckv, 3 s_ckv, 4 w_co, 5 s_co,
+6 cross_norm; an utterance's encoder memory is fp16 N(0,1) [frames][dim]
+under stream 2^40 + utterance.
 """
 import numpy as np
 
 from . import ops
 
 FIELDS = ["w_qkv", "s_qkv", "w_o", "s_o", "w_gu", "s_gu", "w_d", "s_d", "attn_norm", "ffn_norm"]
+CROSS_FIELDS = ["w_cq", "s_cq", "w_ckv", "s_ckv", "w_co", "s_co", "cross_norm"]
+MEMORY_STREAM = 1 << 40
 KV_STREAM_SHIFT = 20
 
 
@@ -40,19 +46,23 @@ def decoder_weights(cfg):
     G, GF = d // 32, F // 32
     shapes = {"w_qkv": (3 * d * d, "i8"), "s_qkv": (3 * d * G, "s"), "w_o": (d * d, "i8"), "s_o": (d * G, "s"),
               "w_gu": (2 * F * d, "i8"), "s_gu": (2 * F * G, "s"), "w_d": (d * F, "i8"), "s_d": (d * GF, "s"),
-              "attn_norm": (d, "n"), "ffn_norm": (d, "n")}
+              "attn_norm": (d, "n"), "ffn_norm": (d, "n"),
+              "w_cq": (d * d, "i8"), "s_cq": (d * G, "s"), "w_ckv": (2 * d * d, "i8"), "s_ckv": (2 * d * G, "s"),
+              "w_co": (d * d, "i8"), "s_co": (d * G, "s"), "cross_norm": (d, "n")}
+
+    def gen(name, stream):
+        count, kind = shapes[name]
+        if kind == "i8":
+            return ops.synth_int8(seed, stream, count)
+        if kind == "s":
+            return ops.synth_uniform_f16(seed, stream, count, 0.001, 0.02)
+        return _norm(seed, stream, count)
+
     layers = []
     for l in range(cfg.layers):
-        t = {}
-        for f, name in enumerate(FIELDS):
-            count, kind = shapes[name]
-            stream = 100 + 16 * l + f
-            if kind == "i8":
-                t[name] = ops.synth_int8(seed, stream, count)
-            elif kind == "s":
-                t[name] = ops.synth_uniform_f16(seed, stream, count, 0.001, 0.02)
-            else:
-                t[name] = _norm(seed, stream, count)
+        t = {name: gen(name, 100 + 16 * l + f) for f, name in enumerate(FIELDS)}
+        if getattr(cfg, "cross", 0):
+            t.update({name: gen(name, 5000 + 16 * l + f) for f, name in enumerate(CROSS_FIELDS)})
         layers.append(t)
     final_norm = _norm(seed, 2, d)
     emb = ops.synth_normal_f16(seed, 1, V * d, scale=0.02)
@@ -66,3 +76,9 @@ def prefix_kv_values(seed, session, layer, kind, count, heads):
     first = ((layer * 2 + kind) << KV_STREAM_SHIFT) * heads * 64
     raw = ops.synth_normal_f16(seed, session, count * heads * 64, first=first)
     return raw.view(np.float16).astype(np.float32).reshape(count, heads, 64)
+
+
+def memory_values(seed, utterance, frames, dim):
+    """fp16 N(0,1) encoder memory of one utterance as float32 [frames][dim]."""
+    raw = ops.synth_normal_f16(seed, MEMORY_STREAM + utterance, frames * dim)
+    return raw.view(np.float16).astype(np.float32).reshape(frames, dim)

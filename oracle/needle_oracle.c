@@ -546,10 +546,19 @@ void ndo_topk_logsoftmax(const float *x, int n, int k, int *indices, float *log_
 
 int ndo_decoder_row(const ndo_decoder *m, int token, int pos, int capacity, int8_t *kv_k, int8_t *kv_v,
                     float *kv_ks, float *kv_vs, const float *rope_cos, const float *rope_sin, float *logits) {
+    return ndo_decoder_row_cross(m, token, pos, capacity, kv_k, kv_v, kv_ks, kv_vs, rope_cos, rope_sin, 0, NULL, NULL,
+                                 NULL, NULL, logits);
+}
+
+int ndo_decoder_row_cross(const ndo_decoder *m, int token, int pos, int capacity, int8_t *kv_k, int8_t *kv_v,
+                          float *kv_ks, float *kv_vs, const float *rope_cos, const float *rope_sin, int frames,
+                          const int8_t *mem_k, const int8_t *mem_v, const float *mem_ks, const float *mem_vs,
+                          float *logits) {
     const int d = m->dim, H = m->heads, hd = m->head_dim, F = m->ffn, V = m->vocab;
     const int width = H * hd;
     const float inv_sqrt = 1.0f / sqrtf((float)hd);
-    size_t floats = (size_t)d * 4 + 3 * (size_t)d + 2 * (size_t)F + F + (size_t)(pos + 1) + 64;
+    const int span = (pos + 1 > frames ? pos + 1 : frames);
+    size_t floats = (size_t)d * 4 + 3 * (size_t)d + 2 * (size_t)F + F + (size_t)span + 64;
     float *buf = (float *)malloc(floats * sizeof(float));
     int8_t *qbuf = (int8_t *)malloc((size_t)(F > d ? F : d) + (size_t)width);
     if (!buf || !qbuf) {
@@ -584,6 +593,21 @@ int ndo_decoder_row(const ndo_decoder *m, int token, int pos, int capacity, int8
         sa = ndo_quantize_int8(o, d, qa);
         ndo_matmul_i8g32(m->w_o[l], m->s_o[l], d, d, qa, &sa, 1, NULL, proj, d);
         for (int i = 0; i < d; i++) x[i] = x[i] + proj[i];
+        if (frames > 0 && m->w_cq) {
+            /* cross block: queries from this row, keys/values from the memory */
+            ndo_rms_norm(x, m->cross_norm[l], d, h);
+            sa = ndo_quantize_int8(h, d, qa);
+            ndo_matmul_i8g32(m->w_cq[l], m->s_cq[l], d, d, qa, &sa, 1, NULL, qkv, d);
+            for (int hh = 0; hh < H; hh++) qs[hh] = ndo_quantize_int8(qkv + hh * hd, hd, qq + hh * hd);
+            const int8_t *mk = mem_k + (size_t)l * frames * width, *mv = mem_v + (size_t)l * frames * width;
+            const float *mks = mem_ks + (size_t)l * frames * H, *mvs = mem_vs + (size_t)l * frames * H;
+            for (int hh = 0; hh < H; hh++)
+                ndo_attention_head(qq + hh * hd, qs[hh], mk + hh * hd, mks + hh, mv + hh * hd, mvs + hh, width, width,
+                                   H, 0, frames - 1, hd, hd, inv_sqrt, scores, o + hh * hd, NULL);
+            sa = ndo_quantize_int8(o, d, qa);
+            ndo_matmul_i8g32(m->w_co[l], m->s_co[l], d, d, qa, &sa, 1, NULL, proj, d);
+            for (int i = 0; i < d; i++) x[i] = x[i] + proj[i];
+        }
         ndo_rms_norm(x, m->ffn_norm[l], d, h);
         sa = ndo_quantize_int8(h, d, qa);
         ndo_matmul_i8g32(m->w_gu[l], m->s_gu[l], 2 * F, d, qa, &sa, 1, NULL, gu, 2 * F);
@@ -600,5 +624,28 @@ int ndo_decoder_row(const ndo_decoder *m, int token, int pos, int capacity, int8
     }
     free(buf);
     free(qbuf);
+    return 0;
+}
+
+int ndo_cross_memory(const ndo_decoder *m, int layer, const float *memory, int frames, int8_t *k, int8_t *v, float *ks,
+                     float *vs) {
+    const int d = m->dim, H = m->heads, hd = m->head_dim, width = H * hd;
+    int8_t *qa = (int8_t *)malloc((size_t)d);
+    float *y = (float *)malloc((size_t)2 * d * sizeof(float));
+    if (!qa || !y) {
+        free(qa);
+        free(y);
+        return -1;
+    }
+    for (int f = 0; f < frames; f++) {
+        float sa = ndo_quantize_int8(memory + (size_t)f * d, d, qa);
+        ndo_matmul_i8g32(m->w_ckv[layer], m->s_ckv[layer], 2 * d, d, qa, &sa, 1, NULL, y, 2 * d);
+        for (int h = 0; h < H; h++) {
+            ks[(size_t)f * H + h] = ndo_quantize_int8(y + h * hd, hd, k + (size_t)f * width + h * hd);
+            vs[(size_t)f * H + h] = ndo_quantize_int8(y + d + h * hd, hd, v + (size_t)f * width + h * hd);
+        }
+    }
+    free(qa);
+    free(y);
     return 0;
 }

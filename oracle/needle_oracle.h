@@ -108,6 +108,11 @@ typedef struct {
     const float *final_norm;                         /* [dim]             */
     const uint16_t *embedding;                       /* fp16 [vocab][dim] */
     const int8_t *w_head; const uint16_t *s_head;    /* [vocab][dim]      */
+    /* cross-attention blocks (Whistle-shaped decoder; NULL w_cq: none):    */
+    const int8_t **w_cq;   const uint16_t **s_cq;    /* [dim][dim]        */
+    const int8_t **w_ckv;  const uint16_t **s_ckv;   /* [2*dim][dim]      */
+    const int8_t **w_co;   const uint16_t **s_co;    /* [dim][dim]        */
+    const float **cross_norm;                        /* [dim]             */
 } ndo_decoder;
 
 /* One decoder layer stack + head for one row at absolute position `pos`.
@@ -118,6 +123,26 @@ typedef struct {
  * and writes logits [vocab]. Returns 0, or -1 if scratch allocation failed. */
 int ndo_decoder_row(const ndo_decoder *m, int token, int pos, int capacity, int8_t *kv_k, int8_t *kv_v,
                     float *kv_ks, float *kv_vs, const float *rope_cos, const float *rope_sin, float *logits);
+
+/* The same row for a decoder with cross-attention blocks: after the
+ * self-attention residual of layer l, x += W_co . Attn(W_cq . RMSNorm(x),
+ * memory of layer l) over all `frames` memory positions (the reference's
+ * cross branch, src/Needle/Engine.cs:1098-1184: Position 0, Window 0,
+ * Frames span).  mem_k/mem_v int8 [layers][frames][heads*head_dim],
+ * mem_ks/mem_vs fp32 [layers][frames][heads]. */
+int ndo_decoder_row_cross(const ndo_decoder *m, int token, int pos, int capacity, int8_t *kv_k, int8_t *kv_v,
+                          float *kv_ks, float *kv_vs, const float *rope_cos, const float *rope_sin, int frames,
+                          const int8_t *mem_k, const int8_t *mem_v, const float *mem_ks, const float *mem_vs,
+                          float *logits);
+
+/* Cross memory of one layer (BuildCrossMemory + per-(frame, head) quantize,
+ * src/Needle/Whistle.cs:886-914,789-790, with int8 projections): every
+ * frame row of `memory` fp32 [frames][dim] is quantized (QuantizeInt8), put
+ * through W_ckv[layer] (I8G32 [2*dim][dim]) and each head's 64 K and 64 V
+ * values are quantized per (frame, head) into k/v [frames][heads*head_dim]
+ * with scales ks/vs [frames][heads]. */
+int ndo_cross_memory(const ndo_decoder *m, int layer, const float *memory, int frames, int8_t *k, int8_t *v, float *ks,
+                     float *vs);
 
 #ifdef __cplusplus
 }

@@ -54,6 +54,8 @@ _SIGS = {
     "ndo_argmax_masked_with_probability": (I, [P, P, I, I, P, _c.POINTER(F)]),
     "ndo_topk_logsoftmax": (None, [P, I, I, P, P, P, I]),
     "ndo_decoder_row": (I, [P, I, I, I, P, P, P, P, P, P, P]),
+    "ndo_decoder_row_cross": (I, [P, I, I, I, P, P, P, P, P, P, I, P, P, P, P, P]),
+    "ndo_cross_memory": (I, [P, I, P, I, P, P, P, P]),
 }
 
 _lib = None
@@ -222,12 +224,16 @@ class _Decoder(_c.Structure):
                 ("rope_theta", F), ("eps", F)] + [
         (name, _c.POINTER(P)) for name in ("w_qkv", "s_qkv", "w_o", "s_o", "w_gu", "s_gu", "w_d", "s_d",
                                            "attn_norm", "ffn_norm")] + [
-        ("final_norm", P), ("embedding", P), ("w_head", P), ("s_head", P)]
+        ("final_norm", P), ("embedding", P), ("w_head", P), ("s_head", P)] + [
+        (name, _c.POINTER(P)) for name in ("w_cq", "s_cq", "w_ckv", "s_ckv", "w_co", "s_co", "cross_norm")]
 
 
 LAYER_TENSORS = {"w_qkv": np.int8, "s_qkv": np.uint16, "w_o": np.int8, "s_o": np.uint16, "w_gu": np.int8,
                  "s_gu": np.uint16, "w_d": np.int8, "s_d": np.uint16, "attn_norm": np.float32,
                  "ffn_norm": np.float32}
+# per-layer tensors of the cross-attention blocks (Whistle-shaped decoder)
+CROSS_TENSORS = {"w_cq": np.int8, "s_cq": np.uint16, "w_ckv": np.int8, "s_ckv": np.uint16, "w_co": np.int8,
+                 "s_co": np.uint16, "cross_norm": np.float32}
 
 
 class Decoder:
@@ -235,11 +241,14 @@ class Decoder:
     copied from the engine under test."""
 
     def __init__(self, cfg, layer_weights, final_norm, embedding, w_head, s_head, capacity):
+        """layer_weights[l] holds LAYER_TENSORS and, for a decoder with
+        cross-attention, CROSS_TENSORS."""
         self.cfg = cfg
         self._keep = []
         L = cfg.layers
+        self.cross = all(n in layer_weights[0] for n in CROSS_TENSORS)
         arrays = {}
-        for name in LAYER_TENSORS:
+        for name in list(LAYER_TENSORS) + (list(CROSS_TENSORS) if self.cross else []):
             arr = (P * L)()
             for l in range(L):
                 a = np.ascontiguousarray(layer_weights[l][name])
@@ -249,11 +258,27 @@ class Decoder:
         self._keep += [arrays]
         g = [np.ascontiguousarray(x) for x in (final_norm, embedding, w_head, s_head)]
         self._keep += g
+        cross = [_c.cast(arrays[n], _c.POINTER(P)) if self.cross else None for n in CROSS_TENSORS]
         self.s = _Decoder(cfg.layers, cfg.dim, cfg.heads, cfg.head_dim, cfg.ffn, cfg.vocab, cfg.rope_theta, 1e-6,
                           *[_c.cast(arrays[n], _c.POINTER(P)) for n in LAYER_TENSORS],
-                          *[x.ctypes.data for x in g])
+                          *[x.ctypes.data for x in g], *cross)
         self.capacity = capacity
         self.cos, self.sin = rope_tables(cfg.rope_theta, cfg.head_dim, capacity)
+
+    def cross_memory(self, memory):
+        """memory fp32 [frames][dim] -> int8 K/V [layers][frames][width] + scales."""
+        c = self.cfg
+        memory = f32(memory)
+        frames, W = memory.shape[0], c.heads * c.head_dim
+        out = {"k": np.zeros((c.layers, frames, W), np.int8), "v": np.zeros((c.layers, frames, W), np.int8),
+               "ks": np.zeros((c.layers, frames, c.heads), np.float32),
+               "vs": np.zeros((c.layers, frames, c.heads), np.float32)}
+        for l in range(c.layers):
+            st = lib().ndo_cross_memory(_c.byref(self.s), l, ptr(memory), frames, ptr(out["k"][l]),
+                                        ptr(out["v"][l]), ptr(out["ks"][l]), ptr(out["vs"][l]))
+            if st != 0:
+                raise MemoryError("oracle scratch allocation failed")
+        return out
 
     def new_kv(self):
         c = self.cfg
@@ -263,10 +288,87 @@ class Decoder:
                 "ks": np.zeros((c.layers, self.capacity, c.heads), np.float32),
                 "vs": np.zeros((c.layers, self.capacity, c.heads), np.float32)}
 
-    def row(self, token, pos, kv):
+    def row(self, token, pos, kv, memory=None):
         logits = np.empty(self.cfg.vocab, np.float32)
-        st = lib().ndo_decoder_row(_c.byref(self.s), token, pos, self.capacity, ptr(kv["k"]), ptr(kv["v"]),
-                                   ptr(kv["ks"]), ptr(kv["vs"]), ptr(self.cos), ptr(self.sin), ptr(logits))
+        if memory is None:
+            st = lib().ndo_decoder_row(_c.byref(self.s), token, pos, self.capacity, ptr(kv["k"]), ptr(kv["v"]),
+                                       ptr(kv["ks"]), ptr(kv["vs"]), ptr(self.cos), ptr(self.sin), ptr(logits))
+        else:
+            frames = memory["k"].shape[1]
+            st = lib().ndo_decoder_row_cross(_c.byref(self.s), token, pos, self.capacity, ptr(kv["k"]),
+                                             ptr(kv["v"]), ptr(kv["ks"]), ptr(kv["vs"]), ptr(self.cos),
+                                             ptr(self.sin), frames, ptr(memory["k"]), ptr(memory["v"]),
+                                             ptr(memory["ks"]), ptr(memory["vs"]), ptr(logits))
         if st != 0:
             raise MemoryError("oracle scratch allocation failed")
         return logits
+
+
+def beam_search(dec, memory, prompt, width, max_steps, eos, length_penalty=1.0, mask_special_023=True):
+    """Whistle.BeamSearch (src/Needle/Whistle.Decode.cs:224-350) on the oracle
+    decoder: per step every live beam's logits give its top-`width`
+    (TopKLogSoftmax, ids 0/2/3 masked), candidates = beam score + log-prob
+    (fp32), sorted by score (descending; equal scores keep (beam, rank)
+    order), EOS candidates join `finished`, at most `width` others stay live;
+    stop when nothing is kept, or when `width` have finished and the best
+    normalised finished score (score / (len+1)^penalty) is at least the best
+    normalised live one; winner = best finished, else best live
+    (score / len^penalty).  Returns (tokens, normalised score)."""
+    c = dec.cfg
+
+    def normalized(score, length):
+        if length_penalty == 0:
+            return np.float32(score)
+        return np.float32(score) / np.float32(np.power(np.float32(length), np.float32(length_penalty)))
+
+    kv = dec.new_kv()
+    logits = None
+    for pos, tok in enumerate(prompt):
+        logits = dec.row(int(tok), pos, kv, memory)
+    live = [(kv, len(prompt), logits)]
+    live_tokens = [[]]
+    live_scores = [np.float32(0.0)]
+    finished = []
+    for _ in range(max_steps):
+        cands = []
+        for i, (_, _, lg) in enumerate(live):
+            idx, lp, _ = topk_logsoftmax(lg, width, mask_special_023=mask_special_023, want_probs=False)
+            for k in range(width):
+                cands.append((np.float32(live_scores[i] + lp[k]), i, int(idx[k]), len(cands)))
+        cands.sort(key=lambda t: (-t[0], t[3]))
+        kept = []
+        for sc, parent, tok, _ in cands:
+            if tok == eos:
+                finished.append((sc, list(live_tokens[parent])))
+            else:
+                kept.append((sc, parent, tok))
+            if len(kept) >= width:
+                break
+        if not kept:
+            break
+        if len(finished) >= width:
+            best_f = max(normalized(s, len(t) + 1) for s, t in finished)
+            best_l = max(normalized(s, len(live_tokens[p]) + 1) for s, p, _ in kept)
+            if best_f >= best_l:
+                break
+        new_live, new_tokens, new_scores = [], [], []
+        for sc, parent, tok in kept:
+            pkv, ppos, _ = live[parent]
+            ckv = {k: v.copy() for k, v in pkv.items()}
+            lg = dec.row(tok, ppos, ckv, memory)
+            new_live.append((ckv, ppos + 1, lg))
+            new_tokens.append(live_tokens[parent] + [tok])
+            new_scores.append(sc)
+        live, live_tokens, live_scores = new_live, new_tokens, new_scores
+    best, best_score = None, -np.inf
+    for sc, toks in finished:
+        v = normalized(sc, len(toks) + 1)
+        if v > best_score:
+            best, best_score = toks, v
+    if best is not None:
+        return best, float(best_score)
+    for sc, toks in zip(live_scores, live_tokens):
+        v = normalized(sc, len(toks))
+        if v > best_score:
+            best, best_score = toks, v
+    return (best or []), float(best_score)

@@ -10,9 +10,12 @@ KV_STREAM_SHIFT = 20
 
 def oracle_decoder(oracle, engine):
     cfg = engine.model
+    names = dict(oracle.LAYER_TENSORS)
+    if getattr(cfg, "cross", 0):
+        names.update(oracle.CROSS_TENSORS)
     layers = []
     for l in range(cfg.layers):
-        layers.append({name: engine.read_tensor(name, dt, layer=l) for name, dt in oracle.LAYER_TENSORS.items()})
+        layers.append({name: engine.read_tensor(name, dt, layer=l) for name, dt in names.items()})
     return oracle.Decoder(cfg, layers, engine.read_tensor("final_norm", np.float32),
                           engine.read_tensor("embedding", np.uint16), engine.read_tensor("w_head", np.int8),
                           engine.read_tensor("s_head", np.uint16), engine.capacity)
@@ -66,6 +69,21 @@ def logits_close(got, ref, atol=1e-3, rtol=1e-2):
     """BASELINE tolerance for logits: max-abs 1e-3 or rel 1e-2 per element."""
     err = np.abs(got - ref)
     return bool(np.all((err <= atol) | (err <= rtol * np.abs(ref)))), float(err.max())
+
+
+def logits_parity(got, ref, atol=1e-3, rtol=1e-2):
+    """Per element within max-abs 1e-3 or rel 1e-2, or else the reference's
+    own logits criterion (tests/Needle.Tests/ParityTests.cs:47-59): cosine
+    similarity above 0.99995 with the same argmax.  The second form covers a
+    row where one int8 quantization step rounded the other way (a value within
+    an ulp of a rounding boundary: the attention sums are not bit-identical),
+    which moves many head logits by a few 1e-3 at once."""
+    ok, err = logits_close(got, ref, atol, rtol)
+    if ok:
+        return True, err
+    g, r = got.astype(np.float64), ref.astype(np.float64)
+    cos = float(g @ r / (np.linalg.norm(g) * np.linalg.norm(r)))
+    return cos > 0.99995 and int(np.argmax(got)) == int(np.argmax(ref)), err
 
 
 def top2_margin(x):
