@@ -494,7 +494,132 @@ def run_serving(args, rank, world, local):
     wl.engine.close()
 
 
-WORKLOADS = {"cfg1": GemvWorkload, "cfg2": DecodeWorkload, "cfg3": ServingWorkload, "cfg5": DecodeWorkload}
+class BeamWorkload:
+    """cfg4: beam search of the Whistle-shaped decoder (4 layers, d 384, 6x64
+    heads, SwiGLU 1536, vocab 51865, cross-attention) for 32 utterances, each
+    with its own fp16 N(0,1) 1500x384 encoder memory projected per layer into
+    int8 K/V pages; beam width 3, up to 128 tokens, score/len (ndl_beam_search:
+    every live beam of every utterance in one step, top-3 log-softmax with
+    ids 0/2/3 masked, forks as slot copies).  A step here is one whole search;
+    value = decoded rows (prompt positions + beam tokens) per second."""
+
+    name = "cfg4_beam_search"
+    PROMPT = [50258, 50259, 50359, 50363]
+
+    def __init__(self, utterances=32, frames=1500, width=3, max_tokens=128, seed=3):
+        self.U, self.frames, self.W, self.max_tokens, self.seed = utterances, frames, width, max_tokens, seed
+        self.unit_bytes = None
+
+    def setup(self, device, rank=0, world=1):
+        eng_mod = __import__("needle_cs_b200.engine", fromlist=["engine"])
+        self.beam_mod = __import__("needle_cs_b200.beam", fromlist=["beam"])
+        U, W = self.U, self.W
+        cap = (self.frames + 63) // 64 * 64
+        beam_pages = (len(self.PROMPT) + self.max_tokens + 63) // 64 + 1
+        pages = U * (cap // 64) + U * 2 * W * beam_pages + 16
+        self.engine = eng_mod.BatchedEngine(eng_mod.whistle_decoder(self.seed), slots=U * (1 + 2 * W),
+                                            context_length=cap, chunk_size=max(U * len(self.PROMPT), U * W),
+                                            max_heads=U * W, kv_pages=pages, device=device.index or 0)
+        self.utt_ids = [rank * U + u for u in range(U)]
+        for u in range(U):
+            self.engine.fill_memory_synthetic(u, self.frames, self.seed, self.utt_ids[u])
+        self.memory_slots = np.arange(U, dtype=np.int32)
+        self.beam_slots = (U + np.arange(U * 2 * W, dtype=np.int32)).reshape(U, 2 * W)
+
+    def search(self, max_tokens=None):
+        st = {}
+        toks, scores = self.beam_mod.beam_search(self.engine, self.memory_slots, self.beam_slots, self.PROMPT,
+                                                 width=self.W, max_steps=max_tokens or self.max_tokens, stats=st)
+        return toks, st["rows"]
+
+    def describe(self):
+        return {"workload": self.name, "model": "synthetic whistle-shaped decoder: 4 layers, d 384, 6x64 heads, "
+                                                "SwiGLU 1536, vocab 51865, cross-attention, int8 weights + fp16 "
+                                                "per-32 scales",
+                "utterances_per_gpu": self.U, "memory": f"fp16 N(0,1) {self.frames}x384 per utterance, int8 K/V "
+                                                         "per (frame, head)", "beam": self.W,
+                "max_tokens": self.max_tokens, "score": "log-prob / length", "prompt": self.PROMPT,
+                "l2": "cross K/V of 32 utterances (~140 MB) exceed L2"}
+
+    def cpu_sample(self, oracle, threads=None):
+        """Oracle beam search of one utterance, a few steps, rows per second
+        (one decoder row per prompt position and live beam token)."""
+        syn = __import__("needle_cs_b200.synthetic", fromlist=["synthetic"])
+        eng_mod = __import__("needle_cs_b200.engine", fromlist=["engine"])
+        model = eng_mod.whistle_decoder(self.seed)
+        layers, fnorm, emb, wh, sh = syn.decoder_weights(model)
+        dec = oracle.Decoder(model, layers, fnorm, emb, wh, sh, 192)
+        mem = dec.cross_memory(syn.memory_values(self.seed, 0, self.frames, model.dim))
+        steps = 4
+        t0 = time.perf_counter()
+        oracle.beam_search(dec, mem, self.PROMPT, self.W, steps, eos=50257)
+        dt = time.perf_counter() - t0
+        rows = len(self.PROMPT) + steps * self.W
+        return rows / dt, 1, (f"1 utterance ({self.frames} frames), beam {self.W}, {steps} steps = {rows} decoder "
+                              f"rows through the scalar C restatement on 1 thread (memory projection untimed)")
+
+
+def run_beam(args, rank, world, local):
+    import torch
+
+    entry.load_package().lib()
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    wl = BeamWorkload()
+    wl.setup(device, rank, world)
+    for _ in range(max(1, args.warmup // 3)):
+        wl.search(max_tokens=8)
+    eng = wl.engine
+    eng.sync()
+    searches = max(1, min(args.steps, 3))
+    barrier(world)
+    torch.cuda.synchronize()
+    stream = torch.cuda.ExternalStream(eng.stream())
+    rows = 0
+    with ClockSampler(torch.cuda.get_device_properties(device).uuid) as clocks:
+        t0 = time.perf_counter()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record(stream)
+        for _ in range(searches):
+            toks, r = wl.search()
+            rows += r
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        wall = time.perf_counter() - t0
+    barrier(world)
+    ms = max_over_ranks(ev0.elapsed_time(ev1), world)
+    value = world * rows / (ms * 1e-3)
+    # kernel-class shares from one more (profiled) search
+    eng.profile(True)
+    eng.profile_read(reset=True)
+    wl.search(max_tokens=32)
+    eng.sync()
+    prof = eng.profile_read(reset=True)
+    eng.profile(False)
+    total_prof = sum(v for v, _ in prof.values()) or 1.0
+    line = {"metric": "beam decode tokens/sec/box", "value": value, "unit": "tokens/s", "n_gpus": world,
+            "steps": searches, "warmup": max(1, args.warmup // 3), "ms_per_step": ms / searches,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8xint8->int32,f32",
+            "data": "synthetic", "config": wl.describe(), "rows_decoded": rows,
+            "mean_winner_tokens": float(np.mean([len(t) for t in toks])),
+            "kernels": {k: {"ms": round(v, 3), "launches": n, "share": round(v / total_prof, 4)}
+                        for k, (v, n) in prof.items()},
+            "roofline": None,
+            "e2e": {"value": world * rows / wall, "unit": "tokens/s",
+                    "h2d_bytes_per_step": rows // searches * 12, "d2h_bytes_per_step": rows // searches * 24},
+            "gpu_launches": rows // (wl.U * wl.W) * (4 * 14 + 6) if rows else 0,
+            "clocks": clocks.summary()}
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        oracle = entry.load_oracle()
+        v, cores, sample = wl.cpu_sample(oracle)
+        line["cpu_baseline"] = {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    eng.close()
+
+
+WORKLOADS = {"cfg1": GemvWorkload, "cfg2": DecodeWorkload, "cfg3": ServingWorkload, "cfg4": BeamWorkload,
+             "cfg5": DecodeWorkload}
 DECODE = ("cfg2", "cfg5")
 
 
@@ -517,6 +642,9 @@ def run_reference(args, rank, world):
         arrivals, prompts, outs, _ = wl.trace(0)
         value, cores, sample = wl.cpu_sample(oracle, arrivals, prompts, outs)
         metric, unit = "serving output tokens/sec/box", "tokens/s"
+    elif args.workload == "cfg4":
+        value, cores, sample = wl.cpu_sample(oracle)
+        metric, unit = "beam decode tokens/sec/box", "tokens/s"
     elif args.workload in DECODE:
         for i in range(max(1, args.steps // 10)):
             v, cores, sample = wl.cpu_sample(oracle)
@@ -719,6 +847,8 @@ def main():
             run_decode(args, rank, world, local)
         elif args.workload == "cfg3":
             run_serving(args, rank, world, local)
+        elif args.workload == "cfg4":
+            run_beam(args, rank, world, local)
         else:
             run_ours(args, rank, world, local)
     finally:

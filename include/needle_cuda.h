@@ -297,14 +297,15 @@ NDL_API int ndl_slot_copy(ndl_engine *e, int dst, int src);
  * when no beam stays live, when width hypotheses finished and the best
  * finished score/(len+1)^length_penalty beats the best live one, or after
  * max_steps.  tokens [utterances][max_steps], lengths, scores (normalised,
- * nullable) receive each utterance's winner. */
+ * nullable) receive each utterance's winner; rows_run (nullable) the rows
+ * (prompt positions and beam tokens) the search decoded. */
 typedef struct {
     int width, max_steps, eos, mask_special_023;
     float length_penalty;
 } ndl_beam_config;
 NDL_API int ndl_beam_search(ndl_engine *e, const ndl_beam_config *cfg, int utterances, const int *memory_slots,
                             const int *beam_slots, const int32_t *prompt, int prompt_len, int32_t *tokens,
-                            int *lengths, float *scores);
+                            int *lengths, float *scores, long long *rows_run);
 
 /* One batched step: EngineCore.ForwardBatch (src/Needle/Engine.cs:2303-2350)
  * via BatchedEngine.ForwardBatch (src/Needle/BatchEngine.cs:34).  Host

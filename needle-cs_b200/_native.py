@@ -66,7 +66,7 @@ SIGNATURES = {
     "ndl_slot_attach_memory": (c_int, [c_void_p, c_int, c_int]),
     "ndl_slot_copy": (c_int, [c_void_p, c_int, c_int]),
     "ndl_beam_search": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_void_p,
-                                c_void_p]),
+                                c_void_p, c_void_p]),
     "ndl_sched_create": (c_int, [c_void_p, c_void_p, c_void_p]),
     "ndl_sched_create_dry": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p]),
     "ndl_sched_destroy": (c_int, [c_void_p]),

@@ -51,7 +51,7 @@ extern "C" {
 
 NDL_API int ndl_beam_search(ndl_engine *e, const ndl_beam_config *cfg, int utterances, const int *memory_slots,
                             const int *beam_slots, const int32_t *prompt, int prompt_len, int32_t *tokens,
-                            int *lengths, float *scores) {
+                            int *lengths, float *scores, long long *rows_run) {
     NDL_REQUIRE(e && cfg && memory_slots && beam_slots && prompt && tokens && lengths, "null argument");
     const int W = cfg->width;
     NDL_REQUIRE(W >= 1 && W <= 8, "width %d outside 1..8", W);
@@ -91,8 +91,10 @@ NDL_API int ndl_beam_search(ndl_engine *e, const ndl_beam_config *cfg, int utter
     for (int u = 0; u < utterances; u++) head_utt[u] = u;
     std::vector<int> ids((size_t)utterances * W * W);
     std::vector<float> logp((size_t)utterances * W * W);
+    long long rows_total = 0;
     for (int step = 0; step < cfg->max_steps; step++) {
         // logits of every live beam (step 0: the prompts), then their top-W
+        rows_total += (long long)rows_tok.size();
         if ((st = ndl_forward_batch(e, rows_tok.data(), rows_slot.data(), (int)rows_tok.size(), heads.data(),
                                     (int)heads.size())) != NDL_OK)
             return st;
@@ -179,6 +181,7 @@ NDL_API int ndl_beam_search(ndl_engine *e, const ndl_beam_config *cfg, int utter
         }
         if (rows_tok.empty()) break;
     }
+    if (rows_run) *rows_run = rows_total;
     // winners
     for (int u = 0; u < utterances; u++) {
         Utt &t = us[u];
