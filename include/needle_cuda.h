@@ -62,6 +62,13 @@ enum {
     NDL_ERR_CANCELLED = 109
 };
 
+/* Failure detection self-test (no reference counterpart): a kernel waits
+ * for an mbarrier phase that never completes; its bounded wait gives up
+ * after `tests` suspend-hinted tests (about a microsecond each), records the
+ * timeout and returns.  Returns NDL_ERR_TIMEOUT, the status every kernel
+ * reports after a wait that ran out; the context stays usable. */
+NDL_API int ndl_selftest_bounded_wait(int tests);
+
 /* Library identity and diagnostics (no reference counterpart). */
 NDL_API const char *ndl_version(void);
 NDL_API const char *ndl_status_string(int status);
@@ -182,6 +189,22 @@ NDL_API int ndl_attention_paged_noalloc(const int8_t *q, const float *qs, const 
                                         const int32_t *row_pos, int rows, int heads, const int32_t *page_table,
                                         int slots, int max_pages, const uint8_t *pool, size_t page_bytes,
                                         int num_pages, int layer, float *out, int *status, void *stream);
+
+/* ------------------------------------------------------------------ */
+/* KernelTable conformance exports                                     */
+/* ------------------------------------------------------------------ */
+/* The reference's kernel slots with their exact Cdecl signatures
+ * (src/Needle/Kernels/KernelTable.cs:5-47, Net10KernelExports.Fill
+ * src/Needle/Kernels/Net10KernelExports.cs:118-150), computed on the current
+ * CUDA device; host pointers, synchronous, safe to call from several
+ * threads.  No error channel, like the slots: NaN / -2 on failure with the
+ * reason in ndl_last_error.
+ *   QuantizeInt8     float(float* x, int n, sbyte* destination)  slot 22
+ *   ArgMaxMasked     int(float* x, uint* mask, int words, int length)  slot 25
+ *   BestProbability  float(float* values, int count, float best)  slot 26 */
+NDL_API float ndl_kt_quantize_int8(const float *x, int n, int8_t *destination);
+NDL_API int ndl_kt_argmax_masked(const float *x, const uint32_t *mask, int words, int length);
+NDL_API float ndl_kt_best_probability(const float *values, int count, float best);
 
 /* ------------------------------------------------------------------ */
 /* Batched decode engine (replaces BatchedEngine + EngineCore slots)   */

@@ -65,6 +65,10 @@ SIGNATURES = {
     "ndl_slot_fill_memory_synthetic": (c_int, [c_void_p, c_int, c_int, c_u64, c_u64]),
     "ndl_slot_attach_memory": (c_int, [c_void_p, c_int, c_int]),
     "ndl_slot_copy": (c_int, [c_void_p, c_int, c_int]),
+    "ndl_selftest_bounded_wait": (c_int, [c_int]),
+    "ndl_kt_quantize_int8": (c_float, [c_void_p, c_int, c_void_p]),
+    "ndl_kt_argmax_masked": (c_int, [c_void_p, c_void_p, c_int, c_int]),
+    "ndl_kt_best_probability": (c_float, [c_void_p, c_int, c_float]),
     "ndl_beam_search": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_void_p,
                                 c_void_p, c_void_p]),
     "ndl_sched_create": (c_int, [c_void_p, c_void_p, c_void_p]),

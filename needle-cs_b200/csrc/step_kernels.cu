@@ -330,4 +330,25 @@ int launch_half_to_float(const uint16_t *src, long long n, float *dst, cudaStrea
     return check_launch("half_to_float");
 }
 
+// BestProbability (src/Needle/Ops.cs:1435-1470): 1 / sum_i exp(x_i - best),
+// one CTA (tree sum; the reference's vector sum order differs: tolerance).
+__global__ void __launch_bounds__(256) best_probability_kernel(const float *__restrict__ x, int count, float best,
+                                                               float *__restrict__ out) {
+    __shared__ float s_sum[256];
+    float acc = 0.0f;
+    for (int i = threadIdx.x; i < count; i += blockDim.x) acc += expf(x[i] - best);
+    s_sum[threadIdx.x] = acc;
+    __syncthreads();
+    for (int s = blockDim.x / 2; s > 0; s >>= 1) {
+        if (threadIdx.x < s) s_sum[threadIdx.x] += s_sum[threadIdx.x + s];
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) out[0] = 1.0f / s_sum[0];
+}
+
+int launch_best_probability(const float *x, int count, float best, float *out, cudaStream_t stream) {
+    best_probability_kernel<<<1, 256, 0, stream>>>(x, count, best, out);
+    return check_launch("best_probability");
+}
+
 }  // namespace ndl
