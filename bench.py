@@ -26,6 +26,12 @@ PEAKS_PATH = os.path.join(ROOT, "MEASURED_PEAKS.json")
 DECODE_METRIC = "decode tokens/sec/box"
 LINEAR_METRIC = "int8 linear GB/s (algorithmic bytes)"
 FALLBACK_HBM_GBS = 6650.0
+# DRAM bytes (read + write) per algorithmic byte of attn_decode_kernel, from a
+# full ncu capture of the cfg5 launch shape on a 2-layer engine
+# (needle-cs_b200/profile_case.py attention: 320.9 MB for 298.2 MB); the
+# excess is the unused tail of each row's last 64-position page, so traffic
+# grows with the algorithmic bytes and scales to the 12-layer launch.
+ATTN_TRAFFIC_PER_ALG_BYTE = 1.076
 
 
 def hbm_peak():
@@ -733,7 +739,10 @@ def run_decode(args, rank, world, local):
             "config": wl.describe(),
             "roofline": {"bound": "hbm", "kernel": "attn_decode_kernel (paged int8 KV, split-K)",
                          "achieved": attn_achieved, "peak": peak, "unit": "GB/s",
-                         "frac": attn_achieved / peak if attn_achieved else None, "traffic": None,
+                         "frac": attn_achieved / peak if attn_achieved else None,
+                         "traffic": ATTN_TRAFFIC_PER_ALG_BYTE * prof_attn_bytes / max(attn_n, 1),
+                         "traffic_source": "ncu capture of the same launch shape (2-layer engine), scaled by "
+                                           "algorithmic bytes",
                          "peak_source": peak_kind, "algorithmic_bytes_per_launch": prof_attn_bytes / max(attn_n, 1),
                          "avg_launch_ms": attn_ms / max(attn_n, 1), "profiled_steps": prof_steps},
             "kernels": kernels, "dominant_kernel_class": dominant,
