@@ -62,6 +62,27 @@ __device__ __forceinline__ float half_to_float_ref_fast(uint16_t h) {
         f = __uint_as_float(((((uint32_t)h & 0x7FFFu) << 13) + 0x38000000u) | ((uint32_t)(h & 0x8000u) << 16));
     return f;
 }
+
+// Packed pairs of fp32 (fma/add.rn.f32x2: each half is an IEEE fma/add with
+// round-to-nearest, the same bits as the scalar forms).
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float &lo, float &hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
 #endif
 
 // IEEE round-to-nearest-even float -> binary16 (integer-only).
