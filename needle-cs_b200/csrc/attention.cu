@@ -263,10 +263,14 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 3) attn_decode_kernel(AttnArg
     // r gives warp w the item r*W + w (even r) or r*W + W-1-w (odd r).
     const int wg = blockIdx.x * kAttnWarps + warp;
     auto item_of = [&](int round) { return round * W + ((round & 1) ? W - 1 - wg : wg); };
-    // producer cursor (lane 0): next page to issue
+    // Producer cursor, kept identically by every lane (the producer steps are
+    // warp-collective).  On entering an item, lanes 0..31 fetch the item's
+    // page ids in one load; lane 0 then takes each page id by shuffle, so a
+    // page's copy is not held up by its page-table load.
     int p_round = -1;
     AttnItem pit{};
     int p_page = 0, p_left = 0;
+    int pid = -1;  // page id of page (first_page + lane) of the producer's item
     unsigned issued = 0;
     auto advance_producer = [&]() -> bool {
         while (p_left == 0) {
@@ -276,28 +280,33 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 3) attn_decode_kernel(AttnArg
             if (i < n_items && attn_item(a, i, pit)) {
                 p_page = pit.first_page;
                 p_left = pit.n_pages;
+                pid = lane < pit.n_pages ? a.page_table[(size_t)pit.slot * a.max_pages + pit.first_page + lane] : -1;
             }
         }
         return true;
     };
-    auto issue_one = [&]() {  // lane 0 only; requires p_left > 0
+    auto issue_one = [&]() {  // all lanes; requires p_left > 0
         uint64_t *bar = &bars[issued % kAttnStages];
-        const int page = a.page_table[(size_t)pit.slot * a.max_pages + p_page];
-        if (page < 0 || page >= a.num_pages) {
-            if (a.status) atomicOr(a.status, kStatusBadPage);
-            asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-        } else {
-            const uint8_t *src = a.pool + (size_t)page * a.page_bytes + kv_block_offset(a.layer, pit.head, a.heads);
-            fence_proxy_async_smem();
-            mbar_arrive_expect_tx(bar, kKvBlockBytes);
-            bulk_g2s(ring + (issued % kAttnStages) * kKvBlockBytes, src, kKvBlockBytes, bar);
+        const int k = p_page - pit.first_page;
+        int page = __shfl_sync(0xffffffffu, pid, k & 31);
+        if (k >= 32) page = a.page_table[(size_t)pit.slot * a.max_pages + p_page];
+        if (lane == 0) {
+            if (page < 0 || page >= a.num_pages) {
+                if (a.status) atomicOr(a.status, kStatusBadPage);
+                asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+            } else {
+                const uint8_t *src =
+                    a.pool + (size_t)page * a.page_bytes + kv_block_offset(a.layer, pit.head, a.heads);
+                fence_proxy_async_smem();
+                mbar_arrive_expect_tx(bar, kKvBlockBytes);
+                bulk_g2s(ring + (issued % kAttnStages) * kKvBlockBytes, src, kKvBlockBytes, bar);
+            }
         }
         issued++;
         p_page++;
         p_left--;
     };
-    if (lane == 0)
-        for (int k = 0; k < kAttnStages && advance_producer(); k++) issue_one();
+    for (int k = 0; k < kAttnStages && advance_producer(); k++) issue_one();
 
     unsigned consumed = 0;
     bool timed_out = false;
@@ -395,7 +404,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 3) attn_decode_kernel(AttnArg
             }
             __syncwarp();
             consumed++;
-            if (lane == 0 && advance_producer()) issue_one();
+            if (advance_producer()) issue_one();
         }
         if (timed_out) break;
         l = warp_sum_f(l);
