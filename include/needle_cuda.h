@@ -278,6 +278,10 @@ NDL_API int ndl_engine_profile(ndl_engine *e, int enable);
 /* Steps are captured as one CUDA graph per (rows, heads) shape and replayed
  * (default on; profiling runs the kernels directly). */
 NDL_API int ndl_engine_use_graphs(ndl_engine *e, int enable);
+/* Step kernels are launched with programmatic dependent launch (default on):
+ * each waits for its predecessor to complete before reading anything, so
+ * results are identical either way; only launch latency overlaps. */
+NDL_API int ndl_engine_use_pdl(ndl_engine *e, int enable);
 NDL_API int ndl_engine_profile_read(ndl_engine *e, double *ms, long long *launches, int reset);
 
 /* Slot state: BatchedEngine.SlotLength/ResetSlot/MarkSlot/RewindSlot

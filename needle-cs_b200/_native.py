@@ -81,6 +81,7 @@ SIGNATURES = {
     "ndl_sched_last_plan": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
     "ndl_engine_profile": (c_int, [c_void_p, c_int]),
     "ndl_engine_use_graphs": (c_int, [c_void_p, c_int]),
+    "ndl_engine_use_pdl": (c_int, [c_void_p, c_int]),
     "ndl_engine_profile_read": (c_int, [c_void_p, c_void_p, c_void_p, c_int]),
 }
 

@@ -54,6 +54,7 @@ __device__ __forceinline__ float warp_quantize64(float lo, float hi, int8_t &qlo
 
 // ------------------------------------------------------------- KV write --
 __global__ void __launch_bounds__(256) kv_write_kernel(KvWriteArgs a) {
+    pdl_enter();
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (warp >= a.rows * a.heads) return;
@@ -109,7 +110,7 @@ __global__ void __launch_bounds__(256) kv_write_kernel(KvWriteArgs a) {
 int launch_kv_write(const KvWriteArgs &a, cudaStream_t stream) {
     int warps = a.rows * a.heads;
     if (warps == 0) return NDL_OK;
-    kv_write_kernel<<<(warps + 7) / 8, 256, 0, stream>>>(a);
+    launch_kernel(kv_write_kernel, dim3((warps + 7) / 8), dim3(256), 0, stream, a);
     return check_launch("kv_write");
 }
 
@@ -118,6 +119,7 @@ int launch_kv_write(const KvWriteArgs &a, cudaStream_t stream) {
 // the memory has no positions) into q8 in k_slot order.  Warp per (row, head).
 __global__ void __launch_bounds__(256) cross_query_kernel(const float *__restrict__ q, int ldq, int heads, int rows,
                                                           int8_t *__restrict__ q8, float *__restrict__ qs) {
+    pdl_enter();
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (warp >= rows * heads) return;
     const int row = warp / heads, head = warp - row * heads;
@@ -133,7 +135,7 @@ __global__ void __launch_bounds__(256) cross_query_kernel(const float *__restric
 int launch_cross_query(const float *q, int ldq, int heads, int rows, int8_t *q8, float *qs, cudaStream_t stream) {
     const int warps = rows * heads;
     if (warps == 0) return NDL_OK;
-    cross_query_kernel<<<(warps + 7) / 8, 256, 0, stream>>>(q, ldq, heads, rows, q8, qs);
+    launch_kernel(cross_query_kernel, dim3((warps + 7) / 8), dim3(256), 0, stream, q, ldq, heads, rows, q8, qs);
     return check_launch("cross_query");
 }
 
@@ -243,6 +245,7 @@ __device__ __forceinline__ void mma_s8u8_m16n8k32(int (&d)[4], const uint4 &a, u
 //    accumulator until the softmax rescale changes; the digits recombine
 //    as D0 * 2^16 + D1 * 2^8 + D2 once per item.
 __global__ void __launch_bounds__(kAttnWarps * 32, 3) attn_decode_kernel(AttnArgs a) {
+    pdl_enter();
     extern __shared__ __align__(128) uint8_t smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int gid = lane >> 2, tig = lane & 3;
@@ -461,6 +464,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 3) attn_decode_kernel(AttnArg
 // w_c = exp(peak_c - max peak), chunks in ascending order.  Warp per
 // (row, head); lane owns dims 2*lane, 2*lane+1.
 __global__ void __launch_bounds__(256) attn_merge_kernel(AttnArgs a) {
+    pdl_enter();
     const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (w >= a.rows * a.heads) return;
     const int row = w / a.heads;
@@ -503,11 +507,11 @@ int launch_attn_decode(const AttnArgs &a, cudaStream_t stream) {
     long long blocks = (items + kAttnWarps - 1) / kAttnWarps;
     const long long resident = (long long)sms * 3;  // three CTAs (12 warps) per SM fit the shared memory
     if (blocks > resident) blocks = resident;
-    attn_decode_kernel<<<(unsigned)blocks, kAttnWarps * 32, smem, stream>>>(a);
+    launch_kernel(attn_decode_kernel, dim3((unsigned)blocks), dim3(kAttnWarps * 32), smem, stream, a);
     int st = check_launch("attn_decode");
     if (st != NDL_OK || a.max_chunks < 2) return st;
     const int warps = a.rows * a.heads;
-    attn_merge_kernel<<<(warps + 7) / 8, 256, 0, stream>>>(a);
+    launch_kernel(attn_merge_kernel, dim3((warps + 7) / 8), dim3(256), 0, stream, a);
     return check_launch("attn_merge");
 }
 

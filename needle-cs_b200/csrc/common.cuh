@@ -7,6 +7,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 #include "../../include/needle_cuda.h"
 
 namespace ndl {
@@ -150,5 +152,49 @@ __host__ __device__ __forceinline__ float synth_uniform(uint64_t key, uint64_t i
 __host__ __device__ __forceinline__ int8_t synth_int8(uint64_t key, uint64_t i) {
     return (int8_t)((int)(synth_hash(key, i) % 255u) - 127);
 }
+
+// ---- programmatic dependent launch (step kernels) ----
+// A step kernel first waits for its predecessor grid to complete
+// (griddepcontrol.wait: a no-op when launched without the attribute), then
+// lets its own dependent launch (griddepcontrol.launch_dependents), so the
+// next kernel's launch overlaps this one's work while memory order is kept.
+#ifdef __CUDACC__
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_enter() {
+    pdl_wait();
+    pdl_trigger();
+}
+#endif
+// Host: launches made while the flag is set (the engine's step) carry the
+// programmatic-stream-serialization attribute.
+inline bool &pdl_flag() {
+    static thread_local bool flag = false;
+    return flag;
+}
+struct PdlScope {
+    bool old;
+    explicit PdlScope(bool on) : old(pdl_flag()) { pdl_flag() = on; }
+    ~PdlScope() { pdl_flag() = old; }
+};
+#ifdef __CUDACC__
+template <typename... KArgs, typename... Args>
+cudaError_t launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                          Args &&...args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    if (pdl_flag()) {
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+    }
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+#endif
 
 }  // namespace ndl

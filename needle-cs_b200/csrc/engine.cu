@@ -114,6 +114,7 @@ struct ndl_engine {
     std::vector<StepGraph> graphs;
     unsigned long long graph_clock = 0;
     bool use_graphs = true;
+    bool use_pdl = true;  // step kernels overlap their launches (programmatic dependent launch)
     // per-kernel-class timing (CUDA events on the engine stream)
     bool profile = false;
     std::vector<cudaEvent_t> event_pool;
@@ -380,6 +381,7 @@ int check_slot(ndl_engine *e, int slot) {
 // The device work of one step.  Every kernel reads its per-step data from
 // d_meta, so the sequence can be captured once per (rows, heads) and replayed.
 int step_kernels(ndl_engine *e, int rows, int heads) {
+    PdlScope pdl(e->use_pdl);
     const ndl_decoder_config &c = e->dc;
     cudaStream_t s = e->stream;
     const int32_t *d_tokens = e->d_meta + e->off_tokens, *d_slot = e->d_meta + e->off_slot;
@@ -910,6 +912,14 @@ NDL_API int ndl_forward_batch(ndl_engine *e, const int *tokens, const int *row_s
     for (int r = 0; r < rows; r++) e->slot_len[m[e->off_slot + r]] = m[e->off_pos + r] + 1;
     e->last_rows = rows;
     e->last_heads = heads;
+    return NDL_OK;
+}
+
+NDL_API int ndl_engine_use_pdl(ndl_engine *e, int enable) {
+    NDL_REQUIRE(e, "engine is NULL");
+    e->use_pdl = enable != 0;
+    for (auto &g : e->graphs) cudaGraphExecDestroy(g.exec);  // graphs captured the old launch form
+    e->graphs.clear();
     return NDL_OK;
 }
 

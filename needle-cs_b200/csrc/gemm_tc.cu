@@ -98,6 +98,7 @@ template <int BT>
 __global__ void __launch_bounds__(kTcThreads, 1)
     gemm_i8g32_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x,
                          TcParams p) {
+    pdl_enter();
     constexpr int EC = BT / 4;  // token columns per epilogue warp
     constexpr int kSlotCols = 4 * BT;
     constexpr int S = TcSmem<BT>::kStages;
@@ -343,7 +344,7 @@ static int launch_bt(const MatmulArgs &a, const TcParams &p, cudaStream_t stream
     const long long tiles = (long long)a.batch * ((a.n + kTcBlockN - 1) / kTcBlockN) * ((a.m + BT - 1) / BT);
     if (tiles > 0x7fffffff) return NDL_ERR_UNSUPPORTED;
     const int grid = (int)std::min<long long>(tiles, tc_sms());
-    gemm_i8g32_tc_kernel<BT><<<grid, kTcThreads, smem, stream>>>(map_w, map_x, p);
+    launch_kernel(gemm_i8g32_tc_kernel<BT>, dim3(grid), dim3(kTcThreads), smem, stream, map_w, map_x, p);
     return check_launch("gemm_i8g32_tc");
 }
 

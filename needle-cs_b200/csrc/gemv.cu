@@ -96,6 +96,7 @@ __device__ __forceinline__ float half_plain(uint16_t h) { return __half2float(__
 // distinct banks), so they are not evicted by the streamed weights and scales.
 template <bool kAcc, bool kFull, bool kSmemA>
 __global__ void __launch_bounds__(kGemvWarps * 32, 5) gemv_i8g32_kernel(MatmulArgs a, int scales_vec) {
+    pdl_enter();
     extern __shared__ __align__(16) int8_t s_act[];
     const int lane = threadIdx.x & 31;
     const int gid = lane >> 2, tig = lane & 3;
@@ -259,7 +260,7 @@ int launch_gemv_i8g32(const MatmulArgs &a, cudaStream_t stream) {
     const int smem = 16 * (a.k + 32);
     const bool sm_a = smem <= 48 * 1024;
     const dim3 blk(kGemvWarps * 32);
-#define NDL_GEMV(ACC, FULL, SMA) gemv_i8g32_kernel<ACC, FULL, SMA><<<grid, blk, SMA ? smem : 0, stream>>>(a, sv)
+#define NDL_GEMV(ACC, FULL, SMA) launch_kernel(gemv_i8g32_kernel<ACC, FULL, SMA>, dim3(grid), dim3(blk), SMA ? smem : 0, stream, a, sv)
     if (a.acc) {
         if (full) { if (sm_a) NDL_GEMV(true, true, true); else NDL_GEMV(true, true, false); }
         else { if (sm_a) NDL_GEMV(true, false, true); else NDL_GEMV(true, false, false); }

@@ -41,6 +41,7 @@ __global__ void __launch_bounds__(256) quantize_rows_vec_kernel(const float *__r
                                                                 const float *__restrict__ weight, int rows,
                                                                 int cols, int8_t *__restrict__ q,
                                                                 float *__restrict__ scales) {
+    pdl_enter();
     int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     int lane = threadIdx.x & 31;
     if (warp >= rows) return;
@@ -104,6 +105,7 @@ __global__ void __launch_bounds__(256) quantize_rows_scalar_kernel(const float *
                                                                    const float *__restrict__ weight, int rows,
                                                                    int cols, int8_t *__restrict__ q,
                                                                    float *__restrict__ scales) {
+    pdl_enter();
     int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     int lane = threadIdx.x & 31;
     if (warp >= rows) return;
@@ -144,6 +146,7 @@ __global__ void __launch_bounds__(kRowThreads) row_quantize_kernel(const float *
                                                                    const float *__restrict__ weight, int cols,
                                                                    int ld_in, int8_t *__restrict__ q,
                                                                    float *__restrict__ scales) {
+    pdl_enter();
     __shared__ float red[kRowThreads / 32];
     const int row = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const float4 *in = reinterpret_cast<const float4 *>(x + (size_t)row * ld_in);
@@ -228,19 +231,19 @@ int launch_quantize_rows(const float *x, const float *weight, int rows, int cols
     const bool row_path = (cols % 4 == 0) && cols <= 4 * kRowThreads * kRowMaxVec && aligned(x, 16) &&
                           aligned(q, 4) && (!weight || aligned(weight, 16));
     if (row_path) {
-        if (weight) row_quantize_kernel<1><<<rows, kRowThreads, 0, stream>>>(x, weight, cols, cols, q, scales);
-        else row_quantize_kernel<0><<<rows, kRowThreads, 0, stream>>>(x, nullptr, cols, cols, q, scales);
+        if (weight) launch_kernel(row_quantize_kernel<1>, dim3(rows), dim3(kRowThreads), 0, stream, x, weight, cols, cols, q, scales);
+        else launch_kernel(row_quantize_kernel<0>, dim3(rows), dim3(kRowThreads), 0, stream, x, nullptr, cols, cols, q, scales);
         return check_launch("row_quantize");
     }
     dim3 block(256);
     dim3 grid((rows + 7) / 8);
     bool vec = (cols % 16 == 0) && aligned(x, 16) && aligned(q, 16) && (!weight || aligned(weight, 16));
     if (weight) {
-        if (vec) quantize_rows_vec_kernel<1><<<grid, block, 0, stream>>>(x, weight, rows, cols, q, scales);
-        else quantize_rows_scalar_kernel<1><<<grid, block, 0, stream>>>(x, weight, rows, cols, q, scales);
+        if (vec) launch_kernel(quantize_rows_vec_kernel<1>, dim3(grid), dim3(block), 0, stream, x, weight, rows, cols, q, scales);
+        else launch_kernel(quantize_rows_scalar_kernel<1>, dim3(grid), dim3(block), 0, stream, x, weight, rows, cols, q, scales);
     } else {
-        if (vec) quantize_rows_vec_kernel<0><<<grid, block, 0, stream>>>(x, nullptr, rows, cols, q, scales);
-        else quantize_rows_scalar_kernel<0><<<grid, block, 0, stream>>>(x, nullptr, rows, cols, q, scales);
+        if (vec) launch_kernel(quantize_rows_vec_kernel<0>, dim3(grid), dim3(block), 0, stream, x, nullptr, rows, cols, q, scales);
+        else launch_kernel(quantize_rows_scalar_kernel<0>, dim3(grid), dim3(block), 0, stream, x, nullptr, rows, cols, q, scales);
     }
     return check_launch("quantize_rows");
 }
@@ -251,7 +254,7 @@ int launch_swiglu_quantize_rows(const float *gu, int rows, int ffn, int8_t *q, f
     if (rows == 0) return NDL_OK;
     if (ffn % 4 != 0 || ffn > 4 * kRowThreads * kRowMaxVec || !aligned(gu, 16) || !aligned(q, 4))
         return NDL_ERR_UNSUPPORTED;
-    row_quantize_kernel<2><<<rows, kRowThreads, 0, stream>>>(gu, nullptr, ffn, 2 * ffn, q, scales);
+    launch_kernel(row_quantize_kernel<2>, dim3(rows), dim3(kRowThreads), 0, stream, gu, nullptr, ffn, 2 * ffn, q, scales);
     return check_launch("swiglu_quantize");
 }
 

@@ -18,6 +18,7 @@ __global__ void __launch_bounds__(256) step_prepare_kernel(const int32_t *__rest
                                                            const int32_t *__restrict__ tokens, int rows,
                                                            const uint16_t *__restrict__ embedding, int vocab,
                                                            int dim, float *__restrict__ x, int *status) {
+    pdl_enter();
     // updates[0] = count, then (slot, index, page) triples
     if (blockIdx.x == 0) {
         const int n_updates = updates[0];
@@ -38,7 +39,7 @@ __global__ void __launch_bounds__(256) step_prepare_kernel(const int32_t *__rest
 int launch_step_prepare(const int32_t *updates, int32_t *page_table, int max_pages, const int32_t *tokens, int rows,
                         const uint16_t *embedding, int vocab, int dim, float *x, int *status, cudaStream_t stream) {
     int blocks = rows > 0 ? rows : 1;
-    step_prepare_kernel<<<blocks, 256, 0, stream>>>(updates, page_table, max_pages, tokens, rows, embedding, vocab,
+    launch_kernel(step_prepare_kernel, dim3(blocks), dim3(256), 0, stream, updates, page_table, max_pages, tokens, rows, embedding, vocab,
                                                      dim, x, status);
     return check_launch("step_prepare");
 }
@@ -55,6 +56,7 @@ __device__ __forceinline__ float warp_max_s(float v) {
 __global__ void __launch_bounds__(256) swiglu_quantize_kernel(const float *__restrict__ gu, int rows, int ffn,
                                                               float *__restrict__ act, int8_t *__restrict__ q,
                                                               float *__restrict__ scales) {
+    pdl_enter();
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (warp >= rows) return;
     const float *g = gu + (size_t)warp * 2 * ffn;
@@ -85,13 +87,14 @@ int launch_swiglu_quantize(const float *gu, int rows, int ffn, float *act, int8_
     if (rows == 0) return NDL_OK;
     int st = launch_swiglu_quantize_rows(gu, rows, ffn, q, scales, stream);
     if (st != NDL_ERR_UNSUPPORTED) return st;
-    swiglu_quantize_kernel<<<(rows + 7) / 8, 256, 0, stream>>>(gu, rows, ffn, act, q, scales);
+    launch_kernel(swiglu_quantize_kernel, dim3((rows + 7) / 8), dim3(256), 0, stream, gu, rows, ffn, act, q, scales);
     return check_launch("swiglu_quantize");
 }
 
 // ---------------------------------------------------------- head gather --
 __global__ void gather_rows_kernel(const float *__restrict__ x, const int32_t *__restrict__ idx, int n, int dim,
                                    float *__restrict__ out) {
+    pdl_enter();
     const int r = blockIdx.x;
     if (r >= n) return;
     const float *src = x + (size_t)idx[r] * dim;
@@ -100,7 +103,7 @@ __global__ void gather_rows_kernel(const float *__restrict__ x, const int32_t *_
 
 int launch_gather_rows(const float *x, const int32_t *idx, int n, int dim, float *out, cudaStream_t stream) {
     if (n == 0) return NDL_OK;
-    gather_rows_kernel<<<n, 128, 0, stream>>>(x, idx, n, dim, out);
+    launch_kernel(gather_rows_kernel, dim3(n), dim3(128), 0, stream, x, idx, n, dim, out);
     return check_launch("gather_rows");
 }
 

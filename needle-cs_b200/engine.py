@@ -197,6 +197,9 @@ class BatchedEngine:
     def use_graphs(self, enable=True):
         call("ndl_engine_use_graphs", self._h, int(enable))
 
+    def use_pdl(self, enable=True):
+        call("ndl_engine_use_pdl", self._h, int(enable))
+
     def profile(self, enable=True):
         call("ndl_engine_profile", self._h, int(enable))
 

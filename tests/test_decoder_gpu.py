@@ -216,3 +216,21 @@ def test_graph_replay_matches_direct_launches(small):
         small.forward_batch([5, 77, 9], [0, 2, 3], [0, 1, 2])
         for i in range(3):
             assert np.array_equal(small.batch_logits_row(i), direct[i])
+
+
+def test_overlapped_launches_match_serial_launches(small):
+    """Programmatic dependent launch only overlaps launch latency: logits with
+    it on (graphs and direct launches) equal those with it off, bit for bit."""
+    small.use_pdl(False)
+    small.use_graphs(False)
+    _fresh(small)
+    small.forward_batch([5, 77, 9, 100], [0, 2, 3, 3], [0, 1, 3])
+    serial = [small.batch_logits_row(i) for i in range(3)]
+    small.use_pdl(True)
+    for graphs in (False, True, True):
+        small.use_graphs(graphs)
+        _fresh(small)
+        small.forward_batch([5, 77, 9, 100], [0, 2, 3, 3], [0, 1, 3])
+        for i in range(3):
+            assert np.array_equal(small.batch_logits_row(i), serial[i]), (graphs, i)
+    small.use_graphs(True)
