@@ -293,7 +293,9 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 3) attn_decode_kernel(AttnArg
         const int k = p_page - pit.first_page;
         int page = __shfl_sync(0xffffffffu, pid, k & 31);
         if (k >= 32) page = a.page_table[(size_t)pit.slot * a.max_pages + p_page];
-        if (lane == 0) {
+        // each stage's copy comes from its own lane: copies issued by one
+        // thread complete one after another
+        if (lane == (int)(issued % kAttnStages)) {
             if (page < 0 || page >= a.num_pages) {
                 if (a.status) atomicOr(a.status, kStatusBadPage);
                 asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
