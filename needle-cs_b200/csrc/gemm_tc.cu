@@ -6,26 +6,31 @@
 //   y[t][n] = (residual) + sa[t] * (fma over g ascending of half(sw[n][g]) * D[t][n][g])
 //
 // Persistent: one CTA per SM walks output tiles of 128 weight rows x BT
-// tokens (BT = 32, or 16 when 32 would leave SMs idle), tokens fastest so
-// concurrent CTAs share weight rows in L2.  The weights are the MMA's M
-// operand, so TMEM lane = output feature n and each epilogue thread owns
-// one n: its fp16 group scales are one contiguous row of sw and its stores
-// are coalesced across the warp.
-//  * warp 0: TMA loads of the weight tile [128 rows][128 B] and the
-//    activation tile [BT rows][128 B] per stage (4 groups), 128-byte
-//    swizzle, running ahead across tiles (no cluster multicast).  Copies
-//    issued by one thread complete one after another, so every load in
-//    flight is issued by its own lane.
-//  * warp 1: allocates all 512 TMEM columns; elect.sync issues one
-//    tcgen05.mma kind::i8 (M 128, N BT, K 32) per 32-column group with
-//    accumulate off, so each accumulator holds exactly D of that group.  A
-//    stage's four groups fill TMEM slot r of a 512 / (4 BT)-slot ring; one
-//    commit per stage both fills the slot and frees shared-memory stage r.
-//  * warps 2..17: epilogue, (TMEM lane quadrant) x (BT / 4 token columns).
-//    Per slot a thread reads its four groups' D, releases the slot and folds
-//    acc = fma(half(sw[n][g]), float(D), acc) in ascending group order, two
-//    tokens per packed f32x2 instruction; the token's activation scale
-//    multiplies once per tile.
+// tokens (BT = 16, 32 or 64, chosen on the host from the shape), tokens
+// fastest so concurrently running CTAs share weight rows in L2.  The weights
+// are the MMA's M operand, so TMEM lane = output feature n and each epilogue
+// thread owns one n: its fp16 group scales are one contiguous row of sw and
+// its stores are coalesced across the warp.
+//  * warp 0 (loads): per shared-memory stage (4 groups = 128 bytes of K) the
+//    weight tile [128 rows][128 B] and the activation tile [BT rows][128 B],
+//    128-byte swizzle, no cluster multicast, 8 stages in flight.  Copies
+//    issued by one thread complete one after another, so stage r's two loads
+//    come from lanes 2r and 2r + 1, in one converged instruction.  Weights
+//    are constant: the first stages' weight loads go out before the wait on
+//    the preceding kernel.
+//  * warps 1..2 (MMA): one thread issues about one tcgen05.mma per 150
+//    cycles, while lanes and warps issue in parallel, so the two warps take
+//    alternate stages and lanes 0..3 each issue one group's MMA (kind::i8,
+//    M 128, N BT, K 32, accumulate off: each accumulator holds exactly D of
+//    one group), then commit it to the TMEM slot's full barrier and to the
+//    stage's empty barrier.
+//  * warps 3..18 (epilogue): (TMEM lane quadrant) x (BT / 4 token columns).
+//    TMEM is a ring of slots of min(4, 128 / BT) groups.  Per group a thread
+//    loads the next group's D while it folds the current one,
+//    acc = fma(half(sw[n][g]), float(D), acc), two tokens per packed f32x2
+//    instruction; a slot is released as soon as its last group is in
+//    registers, and a finished tile (times the token's activation scale,
+//    plus the residual) is written while the next tile's first group loads.
 // Every wait is bounded; on a timeout the CTA records kStatusTimeout, leaves
 // its loops, frees TMEM and exits.
 #include <cudaTypedefs.h>
@@ -39,21 +44,31 @@
 namespace ndl {
 
 constexpr int kTcBlockN = 128;  // weight rows per tile (MMA M, TMEM lanes)
-constexpr int kTcBlockK = 128;  // bytes per stage = 4 groups
+constexpr int kTcBlockK = 128;  // bytes of K per shared-memory stage = 4 groups
+constexpr int kTcStages = 8;    // shared-memory ring depth
+constexpr int kTcMmaWarps = 2;
 constexpr int kTcEpiWarps = 16;
-constexpr int kTcThreads = 64 + 32 * kTcEpiWarps;
+constexpr int kTcEpiWarp0 = 1 + kTcMmaWarps;
+constexpr int kTcThreads = 32 * (kTcEpiWarp0 + kTcEpiWarps);
 constexpr uint32_t kTcTmemCols = 512;
 constexpr int kTcWBytes = kTcBlockN * kTcBlockK;  // 16 KB
 constexpr uint32_t kTcWaitLimit = 1u << 22;  // tests of about a microsecond each: a few seconds
 
-// One stage of shared memory per TMEM slot (4 groups x BT columns), so the
-// MMA commit that fills slot r also frees stage r: S = 512 / (4 BT).
+template <int BT>
+struct TcShape {
+    static constexpr int kGroupsPerSlot = BT >= 64 ? 128 / BT : 4;
+    static constexpr int kSlotCols = kGroupsPerSlot * BT;
+    static constexpr int kSlots = kTcTmemCols / kSlotCols;  // 8 (BT 16) or 4
+    static constexpr int kXBytes = BT * kTcBlockK;
+    static constexpr int kCols = BT / 4;  // token columns per epilogue thread
+};
+
 template <int BT>
 struct TcSmem {
-    static constexpr int kStages = kTcTmemCols / (4 * BT);
-    uint8_t w[kStages][kTcWBytes];      // 1024-byte aligned (swizzle atoms)
-    uint8_t x[kStages][BT * kTcBlockK];  // 2 or 4 KB: stays 1024-aligned
-    uint64_t full[kStages], acc_full[kStages], acc_empty[kStages];
+    uint8_t w[kTcStages][kTcWBytes];               // 1024-byte aligned (swizzle atoms)
+    uint8_t x[kTcStages][TcShape<BT>::kXBytes];    // 2, 4 or 8 KB: stays 1024-aligned
+    uint64_t full[kTcStages], empty[kTcStages];
+    uint64_t acc_full[TcShape<BT>::kSlots], acc_empty[TcShape<BT>::kSlots];
     uint32_t tmem_base;
     volatile int abort;
 };
@@ -93,28 +108,52 @@ __device__ __forceinline__ uint4 tc_scales8(const uint16_t *row, int c8, int G, 
     for (int i = 0; i < 8; i++) h[i] = c8 + i < G ? (uint32_t)__ldg(row + c8 + i) : 0u;
     return make_uint4(h[0] | h[1] << 16, h[2] | h[3] << 16, h[4] | h[5] << 16, h[6] | h[7] << 16);
 }
+// True when one of the eight halves is an infinity or a NaN (exponent 31):
+// those take the exact slow conversion.
+__device__ __forceinline__ bool tc_scales_special(uint4 v) {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    bool sp = false;
+#pragma unroll
+    for (int i = 0; i < 4; i++) sp |= (w[i] & 0x7C00u) == 0x7C00u || (w[i] & 0x7C000000u) == 0x7C000000u;
+    return sp;
+}
 
-template <int BT>
+// acc = fma(s2, float(D), acc) for two tokens, float(D) exact by the
+// 1.5*2^23 trick (|D| < 2^22): one block, so the converted pair is built in a
+// register pair directly.
+__device__ __forceinline__ void tc_fold2(uint64_t &acc, uint32_t d0, uint32_t d1, uint64_t s2, uint64_t neg_magic) {
+    asm("{\n .reg .b32 a, b;\n .reg .b64 t;\n"
+        " add.s32 a, %1, 1262485504;\n add.s32 b, %2, 1262485504;\n"
+        " mov.b64 t, {a, b};\n"
+        " add.rn.f32x2 t, t, %3;\n"
+        " fma.rn.f32x2 %0, %4, t, %0;\n}\n"
+        : "+l"(acc)
+        : "r"(d0), "r"(d1), "l"(neg_magic), "l"(s2));
+}
+
+template <int BT, bool kAccOut, bool kResidual>
 __global__ void __launch_bounds__(kTcThreads, 1)
     gemm_i8g32_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x,
                          TcParams p) {
-    pdl_enter();
-    constexpr int EC = BT / 4;  // token columns per epilogue warp
-    constexpr int kSlotCols = 4 * BT;
-    constexpr int S = TcSmem<BT>::kStages;
-    constexpr uint32_t kXBytes = BT * kTcBlockK;
+    using Sh = TcShape<BT>;
+    constexpr int EC = Sh::kCols, Q = Sh::kGroupsPerSlot, S = Sh::kSlots;
+    constexpr uint32_t kStageBytes = kTcWBytes + Sh::kXBytes;
     extern __shared__ uint8_t smem_raw[];
     TcSmem<BT> &s =
         *reinterpret_cast<TcSmem<BT> *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int G = p.k >> 5;
-    const int n_stages = (G + 3) >> 2;
+    const int n_stages = (G + 3) >> 2;  // shared-memory stages per tile
+    const int slots_per_tile = (G + Q - 1) / Q;
     const int nblk = (p.n + kTcBlockN - 1) / kTcBlockN, tblk = (p.m + BT - 1) / BT;
     const int tiles = p.batch * nblk * tblk;
+    // this CTA's tiles: blockIdx.x, blockIdx.x + gridDim.x, ...
+    const int my_tiles = (int)blockIdx.x < tiles ? (tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+    const int total_stages = my_tiles * n_stages;
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < S; i++)
-            mbar_init(&s.full[i], 1), mbar_init(&s.acc_full[i], 1), mbar_init(&s.acc_empty[i], kTcEpiWarps);
+        for (int i = 0; i < kTcStages; i++) mbar_init(&s.full[i], 1), mbar_init(&s.empty[i], 4);
+        for (int i = 0; i < S; i++) mbar_init(&s.acc_full[i], Q), mbar_init(&s.acc_empty[i], kTcEpiWarps);
         s.abort = 0;
         fence_mbar_init();
         prefetch_tmap(&map_w);
@@ -130,150 +169,195 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const uint32_t tmem = s.tmem_base;
 
     if (warp == 0) {
-        // Producer, warp-converged.  Copies issued by one thread complete one
-        // after another, so stage seq's weight and activation tiles are issued
-        // by lanes 2(seq % S) and 2(seq % S) + 1: every load in flight has its
-        // own thread.  Stage r is reused once the MMAs that read it committed
-        // (acc_full[r]).
-        uint32_t seq = 0;
-        for (int tile = blockIdx.x; tile < tiles && !s.abort; tile += gridDim.x) {
-            const TcTile tt = tc_tile(tile, nblk, tblk);
-            for (int st = 0; st < n_stages; st++, seq++) {
-                const int r = seq % S;
-                if (seq >= (uint32_t)S && !tc_wait(s, &s.acc_full[r], ((seq / S) - 1) & 1)) break;
-                const int lw = 2 * r;
-                if (lane == lw) {
-                    mbar_arrive_expect_tx(&s.full[r], kTcWBytes + kXBytes);
-                    tma_load_3d(s.w[r], &map_w, st * kTcBlockK, tt.n0, tt.bz, &s.full[r]);
-                } else if (lane == lw + 1) {
-                    tma_load_2d(s.x[r], &map_x, st * kTcBlockK, tt.tb * BT, &s.full[r]);
-                }
-                __syncwarp();
+        // Loads.  Stage i of this CTA = K block i % n_stages of its tile
+        // number i / n_stages; ring position i % kTcStages.
+        const int first = min(kTcStages, total_stages);
+        int tile = blockIdx.x, st = 0;
+        TcTile tt = tc_tile(tile, nblk, tblk);
+        for (int i = 0; i < first; i++) {  // constant weights: before the dependency wait
+            if (lane == 2 * i) {
+                mbar_arrive_expect_tx(&s.full[i], kStageBytes);
+                tma_load_3d(s.w[i], &map_w, st * kTcBlockK, tt.n0, tt.bz, &s.full[i]);
             }
+            if (++st == n_stages) st = 0, tile += gridDim.x, tt = tc_tile(tile, nblk, tblk);
         }
-    } else if (warp == 1) {
-        // MMA issuer, warp-converged with elect.sync: one commit per stage
-        const uint32_t idesc = idesc_i8(kTcBlockN, BT);
-        uint32_t seq = 0;
-        for (int tile = blockIdx.x; tile < tiles && !s.abort; tile += gridDim.x) {
-            for (int st = 0; st < n_stages && !s.abort; st++, seq++) {
-                const int r = seq % S;
-                if (!tc_wait(s, &s.full[r], (seq / S) & 1)) break;
-                if (seq >= (uint32_t)S && !tc_wait(s, &s.acc_empty[r], ((seq / S) - 1) & 1)) break;
+        __syncwarp();
+        pdl_wait();
+        pdl_trigger();
+        tile = blockIdx.x, st = 0;
+        tt = tc_tile(tile, nblk, tblk);
+        for (int i = 0; i < total_stages && !s.abort; i++) {
+            const int r = i % kTcStages;
+            const bool refill = i >= kTcStages;
+            if (refill) {
+                if (!tc_wait(s, &s.empty[r], ((i / kTcStages) - 1) & 1)) break;
+                if (lane == 2 * r) mbar_arrive_expect_tx(&s.full[r], kStageBytes);
                 __syncwarp();
-                tc_fence_after();
-                const uint64_t dw = sw128_kmajor_desc(s.w[r]), dx = sw128_kmajor_desc(s.x[r]);
-                const int groups = min(4, G - 4 * st);
-                for (int j = 0; j < groups; j++)
-                    mma_i8_elect(tmem + (uint32_t)(r * kSlotCols + j * BT), dw + (uint64_t)(j * 2),
-                                 dx + (uint64_t)(j * 2), idesc);
-                mma_commit_elect(&s.acc_full[r]);
             }
+            const bool wl = refill && lane == 2 * r, xl = lane == 2 * r + 1;
+            if (wl || xl)
+                tma_load_3d(wl ? (void *)s.w[r] : (void *)s.x[r], wl ? &map_w : &map_x, st * kTcBlockK,
+                            wl ? tt.n0 : tt.tb * BT, wl ? tt.bz : 0, &s.full[r]);
+            __syncwarp();
+            if (++st == n_stages) st = 0, tile += gridDim.x, tt = tc_tile(tile, nblk, tblk);
+        }
+    } else if (warp <= kTcMmaWarps) {
+        // MMA: warp 1 + w takes stages w, w + kTcMmaWarps, ...; lane j < 4
+        // issues group j of the stage and commits it.
+        const uint32_t idesc = idesc_i8(kTcBlockN, BT);
+        int lt = 0, st = warp - 1;  // stage i = lt * n_stages + st
+        while (st >= n_stages) st -= n_stages, lt++;
+        for (int i = warp - 1; i < total_stages && !s.abort; i += kTcMmaWarps) {
+            const int r = i % kTcStages;
+            if (!tc_wait(s, &s.full[r], (i / kTcStages) & 1)) break;
+            const int groups = min(4, G - 4 * st);
+            const int nsl = (groups + Q - 1) / Q;  // TMEM slots this stage fills
+            const int sl0 = lt * slots_per_tile + (4 * st) / Q;
+            bool ok = true;
+            for (int k = 0; k < nsl && ok; k++) {
+                const int sq = sl0 + k;
+                if (sq >= S) ok = tc_wait(s, &s.acc_empty[sq % S], ((sq / S) - 1) & 1);
+            }
+            if (!ok) break;
+            tc_fence_after();
+            if (lane < 4) {
+                const int sq = sl0 + lane / Q;
+                if (lane < groups)
+                    mma_i8(tmem + (uint32_t)((sq % S) * Sh::kSlotCols + (lane % Q) * BT),
+                           sw128_kmajor_desc(s.w[r]) + (uint64_t)(lane * 2), sw128_kmajor_desc(s.x[r]) + (uint64_t)(lane * 2),
+                           idesc, 0u);
+                if (lane / Q < nsl) mma_commit(&s.acc_full[sq % S]);
+                mma_commit(&s.empty[r]);
+            }
+            __syncwarp();
+            st += kTcMmaWarps;
+            while (st >= n_stages) st -= n_stages, lt++;
         }
     } else {
-        const int quad = warp & 3, c0 = ((warp - 2) >> 2) * EC;
+        // Epilogue.  Loads run one group ahead of the arithmetic; groups go
+        // in pairs (even: dA, odd: dB; G is even) inside 8-group scale chunks,
+        // so buffers, scale halves and slot boundaries are fixed at compile time.
+        const int quad = warp & 3, c0 = ((warp - kTcEpiWarp0) >> 2) * EC;
         const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)c0;
         const bool vec = p.sw_vec != 0;
         const uint64_t neg_magic = f2_pack(-12582912.0f, -12582912.0f);
-        uint32_t seq = 0;
-        bool ok = true;
-        // first scale chunk of the next tile, loaded one tile ahead
-        uint4 sc_first = make_uint4(0u, 0u, 0u, 0u);
-        if ((int)blockIdx.x < tiles) {
-            const TcTile t0 = tc_tile(blockIdx.x, nblk, tblk);
-            const int n = min(t0.n0 + quad * 32 + lane, p.n - 1);
-            sc_first = tc_scales8(p.sw + (long long)t0.bz * p.sw_stride + (size_t)n * G, 0, G, vec);
-        }
-        for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
-            const TcTile tt = tc_tile(tile, nblk, tblk);
-            const int n = tt.n0 + quad * 32 + lane;
-            const bool nv = n < p.n;
-            const uint16_t *srow = p.sw + (long long)tt.bz * p.sw_stride + (size_t)(nv ? n : 0) * G;
-            uint4 sc = sc_first;
-            uint4 sc_next = G > 8 ? tc_scales8(srow, 8, G, vec) : make_uint4(0u, 0u, 0u, 0u);
-            if (tile + (int)gridDim.x < tiles) {
-                const TcTile tn = tc_tile(tile + gridDim.x, nblk, tblk);
-                const int nn = min(tn.n0 + quad * 32 + lane, p.n - 1);
-                sc_first = tc_scales8(p.sw + (long long)tn.bz * p.sw_stride + (size_t)nn * G, 0, G, vec);
+        pdl_wait();
+        pdl_trigger();
+        uint32_t lsq = 0xFFFFFFFFu;  // TMEM slot sequence of the latest load
+        // load group g (slot position g % Q); a slot's first group waits for its MMAs
+        auto load_group = [&](int g, uint32_t(&d)[EC]) -> bool {
+            if (g % Q == 0) {
+                lsq++;
+                if (!tc_wait(s, &s.acc_full[lsq % S], (lsq / S) & 1)) return false;
+                tc_fence_after();
             }
-            // this tile's activation scales and residuals, needed at the end
-            float sa[EC], res[EC];
+            tmem_ld<EC>(lane_base + (lsq % S) * Sh::kSlotCols + (uint32_t)((g % Q) * BT), d);
+            return true;
+        };
+        // after the wait for group g's load: release its slot if g was the slot's last group
+        auto release = [&](int g) {
+            if (g % Q == Q - 1 || g == G - 1) {
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&s.acc_empty[lsq % S]);
+            }
+        };
+        auto scale_row = [&](int tile) {
+            const TcTile tn = tc_tile(tile, nblk, tblk);
+            const int nn = min(tn.n0 + quad * 32 + lane, p.n - 1);
+            return p.sw + (long long)tn.bz * p.sw_stride + (size_t)nn * G;
+        };
+        uint32_t dA[EC], dB[EC];
+        uint4 sc_nx = make_uint4(0u, 0u, 0u, 0u);
+        bool ok = my_tiles > 0;
+        if (ok) {
+            sc_nx = tc_scales8(scale_row(blockIdx.x), 0, G, vec);
+            ok = load_group(0, dA);
+            if (ok) {
+                tmem_ld_wait(dA);
+                release(0);
+            }
+        }
+        for (int lt = 0; lt < my_tiles && ok; lt++) {
+            const TcTile tt = tc_tile(blockIdx.x + lt * gridDim.x, nblk, tblk);
+            const int n = tt.n0 + quad * 32 + lane, t0 = tt.tb * BT + c0;
+            const bool nv = n < p.n, more_tiles = lt + 1 < my_tiles;
+            const uint16_t *srow = p.sw + (long long)tt.bz * p.sw_stride + (size_t)min(n, p.n - 1) * G;
+            // activation scales (lane c holds token t0 + c) and residuals: used at the end
+            const float sa_l = lane < EC && t0 + lane < p.m ? __ldg(p.sa + t0 + lane) : 0.0f;
+            float res[kResidual ? EC : 1];
+            if constexpr (kResidual) {
 #pragma unroll
-            for (int c = 0; c < EC; c++) {
-                const int t = tt.tb * BT + c0 + c;
-                const bool ok_t = t < p.m && nv;
-                sa[c] = ok_t ? __ldg(p.sa + t) : 0.0f;
-                res[c] = ok_t && p.residual ? p.residual[(size_t)t * p.ldy + n] : 0.0f;
+                for (int c = 0; c < EC; c++)
+                    res[c] = nv && t0 + c < p.m ? p.residual[(size_t)(t0 + c) * p.ldy + n] : 0.0f;
             }
             uint64_t acc[EC / 2];
 #pragma unroll
             for (int c = 0; c < EC / 2; c++) acc[c] = 0ull;
-            for (int st = 0; st < n_stages; st++, seq++) {
-                const int r = seq % S;
-                if (!tc_wait(s, &s.acc_full[r], (seq / S) & 1)) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-                const int groups = min(4, G - 4 * st);
-                // all four groups' D in registers with one wait, then the slot is released
-                uint32_t d[4][EC];
+            auto fold = [&](const uint32_t(&d)[EC], uint4 sc, int gi, bool special, int g) {
+                const uint32_t hw = gi < 2 ? sc.x : gi < 4 ? sc.y : gi < 6 ? sc.z : sc.w;
+                const uint16_t h = (uint16_t)((gi & 1) ? hw >> 16 : hw & 0xFFFFu);
+                float scale = __half2float(__ushort_as_half(h));
+                if (special) scale = half_to_float_ref_fast(h);
+                const uint64_t s2 = f2_pack(scale, scale);
 #pragma unroll
-                for (int j = 0; j < 4; j++)
-                    if (j < groups) tmem_ld<EC>(lane_base + (uint32_t)(r * kSlotCols + j * BT), d[j]);
-                tmem_ld_wait();
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&s.acc_empty[r]);
-                // scales of groups 4st..4st+3: half (st & 1) of the current 8-group chunk
-                const uint32_t w01 = (st & 1) ? sc.z : sc.x, w23 = (st & 1) ? sc.w : sc.y;
+                for (int c = 0; c < EC / 2; c++) tc_fold2(acc[c], d[2 * c], d[2 * c + 1], s2, neg_magic);
+                if constexpr (kAccOut) {  // int32 accumulators of every group (parity checks)
+                    if (nv) {
 #pragma unroll
-                for (int j = 0; j < 4; j++) {
-                    if (j >= groups) break;
-                    const uint32_t hw = j < 2 ? w01 : w23;
-                    const float scale = half_to_float_ref_fast((uint16_t)((j & 1) ? hw >> 16 : hw & 0xFFFFu));
-                    const uint64_t sc2 = f2_pack(scale, scale);
-                    // acc = fma(sw, float(D), acc); float(D) exact by the 1.5*2^23 trick
-#pragma unroll
-                    for (int c = 0; c < EC / 2; c++) {
-                        const uint64_t dv = f2_add(f2_pack(__int_as_float((int)d[j][2 * c] + 0x4B400000),
-                                                           __int_as_float((int)d[j][2 * c + 1] + 0x4B400000)),
-                                                   neg_magic);
-                        acc[c] = f2_fma(sc2, dv, acc[c]);
-                    }
-                    if (p.acc && nv) {  // optional int32 accumulator output (parity checks)
-                        const int g = 4 * st + j;
-#pragma unroll
-                        for (int c = 0; c < EC; c++) {
-                            const int t = tt.tb * BT + c0 + c;
-                            if (t < p.m) p.acc[((size_t)t * p.n + n) * G + g] = (int)d[j][c];
-                        }
+                        for (int c = 0; c < EC; c++)
+                            if (t0 + c < p.m) p.acc[((size_t)(t0 + c) * p.n + n) * G + g] = (int)d[c];
                     }
                 }
-                if (st & 1) {  // next 8-group chunk
-                    sc = sc_next;
-                    const int c8 = 8 * ((st >> 1) + 2);
-                    if (c8 < G) sc_next = tc_scales8(srow, c8, G, vec);
+            };
+            for (int c8 = 0; c8 < G && ok; c8 += 8) {
+                const uint4 sc = sc_nx;
+                const bool special = tc_scales_special(sc);
+                if (c8 + 8 < G) sc_nx = tc_scales8(srow, c8 + 8, G, vec);
+                else if (more_tiles) sc_nx = tc_scales8(scale_row(blockIdx.x + (lt + 1) * gridDim.x), 0, G, vec);
+#pragma unroll
+                for (int gi = 0; gi < 8; gi += 2) {
+                    const int g = c8 + gi;
+                    if (g >= G) break;
+                    // group g is in dA; g + 1 (G is even) loads into dB meanwhile
+                    ok = load_group(g + 1, dB);
+                    fold(dA, sc, gi, special, g);
+                    if (!ok) break;
+                    tmem_ld_wait(dB);
+                    release(g + 1);
+                    // g + 1 is in dB; next into dA: g + 2, or the next tile's group 0
+                    const bool last = g + 2 >= G;
+                    const bool next = !last || more_tiles;
+                    if (next) ok = load_group(last ? 0 : g + 2, dA);
+                    fold(dB, sc, gi + 1, special, g + 1);
+                    if (!ok) break;
+                    if (next) {
+                        tmem_ld_wait(dA);
+                        release(last ? 0 : g + 2);
+                    }
                 }
             }
-            if (!ok || s.abort) break;
-            if (nv) {
-                float *y = p.y + (long long)tt.bz * p.y_stride;
+            if (!ok) break;
+            // tile done: y = (residual) + acc * sa
+            float *y = p.y + (long long)tt.bz * p.y_stride;
 #pragma unroll
-                for (int c = 0; c < EC / 2; c++) {
-                    float v[2];
-                    f2_unpack(acc[c], v[0], v[1]);
+            for (int c = 0; c < EC / 2; c++) {
+                float v[2];
+                f2_unpack(acc[c], v[0], v[1]);
 #pragma unroll
-                    for (int e = 0; e < 2; e++) {
-                        const int t = tt.tb * BT + c0 + 2 * c + e;
-                        if (t < p.m) {
-                            const float out = __fmul_rn(v[e], sa[2 * c + e]);
-                            y[(size_t)t * p.ldy + n] = p.residual ? __fadd_rn(res[2 * c + e], out) : out;
-                        }
+                for (int e = 0; e < 2; e++) {
+                    const int cc = 2 * c + e;
+                    const float sat = __shfl_sync(0xffffffffu, sa_l, cc);
+                    if (nv && t0 + cc < p.m) {
+                        const float out = __fmul_rn(v[e], sat);
+                        float r = out;
+                        if constexpr (kResidual) r = __fadd_rn(res[cc], out);
+                        y[(size_t)(t0 + cc) * p.ldy + n] = r;
                     }
                 }
             }
         }
+        tmem_ld_wait();
     }
     tc_fence_before();
     __syncthreads();
@@ -324,41 +408,73 @@ static int tc_sms() {
     return sms;
 }
 
-template <int BT>
+template <int BT, bool kAccOut, bool kResidual>
 static int launch_bt(const MatmulArgs &a, const TcParams &p, cudaStream_t stream) {
+    auto kernel = gemm_i8g32_tc_kernel<BT, kAccOut, kResidual>;
     const size_t smem = sizeof(TcSmem<BT>) + 1024;
     static bool configured = false;
     if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_i8g32_tc_kernel<BT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)smem);
+        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return set_error(NDL_ERR_CUDA, "gemm smem attribute: %s", cudaGetErrorString(e));
         configured = true;
     }
     CUtensorMap map_w, map_x;
-    // weights [batch][n][k] (a 3-D map even for batch 1: the kernel issues
-    // 3-D loads), activations [m][k] (2-D)
+    // weights [batch][n][k], activations [1][m][k]: both 3-D, so one load
+    // instruction serves either
     int st = make_map(&map_w, a.w, a.k, a.n, a.batch, a.batch > 1 ? a.w_stride : 0, kTcBlockN, 3);
     if (st != NDL_OK) return st;
-    st = make_map(&map_x, a.q, a.k, a.m, 1, 0, BT, 2);
+    st = make_map(&map_x, a.q, a.k, a.m, 1, 0, BT, 3);
     if (st != NDL_OK) return st;
     const long long tiles = (long long)a.batch * ((a.n + kTcBlockN - 1) / kTcBlockN) * ((a.m + BT - 1) / BT);
     if (tiles > 0x7fffffff) return NDL_ERR_UNSUPPORTED;
     const int grid = (int)std::min<long long>(tiles, tc_sms());
-    launch_kernel(gemm_i8g32_tc_kernel<BT>, dim3(grid), dim3(kTcThreads), smem, stream, map_w, map_x, p);
+    launch_kernel(kernel, dim3(grid), dim3(kTcThreads), smem, stream, map_w, map_x, p);
     return check_launch("gemm_i8g32_tc");
+}
+
+template <int BT>
+static int launch_bt(const MatmulArgs &a, const TcParams &p, cudaStream_t stream) {
+    if constexpr (BT == 64) {
+        return a.acc ? launch_bt<64, true, false>(a, p, stream) : launch_bt<64, false, false>(a, p, stream);
+    } else {
+        if (a.acc) return a.residual ? launch_bt<BT, true, true>(a, p, stream) : launch_bt<BT, true, false>(a, p, stream);
+        return a.residual ? launch_bt<BT, false, true>(a, p, stream) : launch_bt<BT, false, false>(a, p, stream);
+    }
+}
+
+// Token tile: per 128-row x BT-token group an SM spends about the longer of
+// the epilogue's fold (~28 / 36 / 46 elements per cycle at BT 16 / 32 / 64)
+// and the MMA issue (~60 cycles), times the waves of tiles over the SMs;
+// ties go to the larger tile (fewer weight re-reads from L2).
+static int pick_bt(const MatmulArgs &a) {
+    const int bts[3] = {16, 32, 64};
+    const double rate[3] = {28.0, 36.0, 46.0};
+    const long long nblk = (long long)a.batch * ((a.n + kTcBlockN - 1) / kTcBlockN);
+    int best = 16;
+    double best_t = 1e300;
+    for (int i = 0; i < 3; i++) {
+        const long long tiles = nblk * ((a.m + bts[i] - 1) / bts[i]);
+        const long long waves = (tiles + tc_sms() - 1) / tc_sms();
+        const double t = (double)waves * std::max(60.0, 128.0 * bts[i] / rate[i]);
+        if (t <= best_t) best_t = t, best = bts[i];
+    }
+    return best;
 }
 
 int launch_gemm_i8g32_tc(const MatmulArgs &a, cudaStream_t stream) {
     if (a.m < 64) return NDL_ERR_UNSUPPORTED;
     if (a.w_stride % 16 != 0) return NDL_ERR_UNSUPPORTED;
     const int G = a.k >> 5;
+    if (G % 2 != 0) return NDL_ERR_UNSUPPORTED;  // groups go in pairs
     const bool sw_vec = G % 8 == 0 && aligned(a.sw, 16) && (a.sw_stride * 2) % 16 == 0;
     TcParams p{a.m,     a.n, a.k,        a.ldy, a.batch,    a.sa, a.sw, a.sw_stride, a.y_stride, a.y, a.residual,
                a.acc, a.status, sw_vec ? 1 : 0};
-    // 32-token tiles when they still give every SM a tile, else 16
-    const long long nblk = (long long)a.batch * ((a.n + kTcBlockN - 1) / kTcBlockN);
-    if (nblk * ((a.m + 31) / 32) >= tc_sms()) return launch_bt<32>(a, p, stream);
-    return launch_bt<16>(a, p, stream);
+    switch (pick_bt(a)) {
+        // a residual's registers do not fit beside 64-token tiles
+        case 64: return a.residual ? launch_bt<32>(a, p, stream) : launch_bt<64>(a, p, stream);
+        case 32: return launch_bt<32>(a, p, stream);
+        default: return launch_bt<16>(a, p, stream);
+    }
 }
 
 }  // namespace ndl

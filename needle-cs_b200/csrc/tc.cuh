@@ -125,6 +125,14 @@ __device__ __forceinline__ void tmem_ld(uint32_t taddr, uint32_t (&r)[N]) {
     else tmem_ld16(taddr, r);
 }
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// Waits for this thread's TMEM loads and ties the destination registers to
+// the wait, so no use of them can be scheduled above it.
+template <int N>
+__device__ __forceinline__ void tmem_ld_wait(uint32_t (&r)[N]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < N; i++) asm volatile("" : "+r"(r[i]));
+}
 
 // Shared-memory matrix descriptor: K-major operand in the 128-byte swizzled
 // canonical layout (8-row x 128-byte atoms, 1024 bytes apart), Blackwell
