@@ -11,20 +11,23 @@
 // are the MMA's M operand, so TMEM lane = output feature n and each epilogue
 // thread owns one n: its fp16 group scales are one contiguous row of sw and
 // its stores are coalesced across the warp.
-//  * warp 0 (loads): per shared-memory stage (4 groups = 128 bytes of K) the
-//    weight tile [128 rows][128 B] and the activation tile [BT rows][128 B],
-//    128-byte swizzle, no cluster multicast, 8 stages in flight.  Copies
-//    issued by one thread complete one after another, so stage r's two loads
-//    come from lanes 2r and 2r + 1, in one converged instruction.  Weights
-//    are constant: the first stages' weight loads go out before the wait on
+//  * warps 0..1 (loads, even / odd stages): per shared-memory stage (4
+//    groups = 128 bytes of K) the weight tile [128 rows][128 B] and the
+//    activation tile [BT rows][128 B], 128-byte swizzle, no cluster
+//    multicast, 8 stages in flight.  Copies issued by one thread complete one
+//    after another, so stage r's two loads come from lanes 2r and 2r + 1, in
+//    one converged instruction; the first 8 stages go out together.  Weights
+//    are constant: those stages' weight loads are issued before the wait on
 //    the preceding kernel.
-//  * warps 1..2 (MMA): one thread issues about one tcgen05.mma per 150
+//  * warps 2..3 (MMA): one thread issues about one tcgen05.mma per 150
 //    cycles, while lanes and warps issue in parallel, so the two warps take
 //    alternate stages and lanes 0..3 each issue one group's MMA (kind::i8,
 //    M 128, N BT, K 32, accumulate off: each accumulator holds exactly D of
 //    one group), then commit it to the TMEM slot's full barrier and to the
 //    stage's empty barrier.
-//  * warps 3..18 (epilogue): (TMEM lane quadrant) x (BT / 4 token columns).
+//  * warps 4..11 (epilogue): (TMEM lane quadrant) x (BT / 2 token columns).
+//    Three warps per scheduler leave the issuing warps their share of issue
+//    slots and each epilogue thread up to 168 registers.
 //    TMEM is a ring of slots of min(4, 128 / BT) groups.  Per group a thread
 //    loads the next group's D while it folds the current one,
 //    acc = fma(half(sw[n][g]), float(D), acc), two tokens per packed f32x2
@@ -46,9 +49,10 @@ namespace ndl {
 constexpr int kTcBlockN = 128;  // weight rows per tile (MMA M, TMEM lanes)
 constexpr int kTcBlockK = 128;  // bytes of K per shared-memory stage = 4 groups
 constexpr int kTcStages = 8;    // shared-memory ring depth
+constexpr int kTcLoadWarps = 2;
 constexpr int kTcMmaWarps = 2;
-constexpr int kTcEpiWarps = 16;
-constexpr int kTcEpiWarp0 = 1 + kTcMmaWarps;
+constexpr int kTcEpiWarps = 8;
+constexpr int kTcEpiWarp0 = kTcLoadWarps + kTcMmaWarps;
 constexpr int kTcThreads = 32 * (kTcEpiWarp0 + kTcEpiWarps);
 constexpr uint32_t kTcTmemCols = 512;
 constexpr int kTcWBytes = kTcBlockN * kTcBlockK;  // 16 KB
@@ -60,7 +64,7 @@ struct TcShape {
     static constexpr int kSlotCols = kGroupsPerSlot * BT;
     static constexpr int kSlots = kTcTmemCols / kSlotCols;  // 8 (BT 16) or 4
     static constexpr int kXBytes = BT * kTcBlockK;
-    static constexpr int kCols = BT / 4;  // token columns per epilogue thread
+    static constexpr int kCols = BT / 2;  // token columns per epilogue thread
 };
 
 template <int BT>
@@ -118,17 +122,10 @@ __device__ __forceinline__ bool tc_scales_special(uint4 v) {
     return sp;
 }
 
-// acc = fma(s2, float(D), acc) for two tokens, float(D) exact by the
-// 1.5*2^23 trick (|D| < 2^22): one block, so the converted pair is built in a
-// register pair directly.
-__device__ __forceinline__ void tc_fold2(uint64_t &acc, uint32_t d0, uint32_t d1, uint64_t s2, uint64_t neg_magic) {
-    asm("{\n .reg .b32 a, b;\n .reg .b64 t;\n"
-        " add.s32 a, %1, 1262485504;\n add.s32 b, %2, 1262485504;\n"
-        " mov.b64 t, {a, b};\n"
-        " add.rn.f32x2 t, t, %3;\n"
-        " fma.rn.f32x2 %0, %4, t, %0;\n}\n"
-        : "+l"(acc)
-        : "r"(d0), "r"(d1), "l"(neg_magic), "l"(s2));
+// acc = fma(s2, float(D), acc) for two tokens; the conversion is exact
+// (|D| <= 2^19 < 2^24).
+__device__ __forceinline__ void tc_fold2(uint64_t &acc, uint32_t d0, uint32_t d1, uint64_t s2) {
+    acc = f2_fma(s2, f2_pack(__int2float_rn((int)d0), __int2float_rn((int)d1)), acc);
 }
 
 template <int BT, bool kAccOut, bool kResidual>
@@ -168,46 +165,53 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     tc_fence_after();
     const uint32_t tmem = s.tmem_base;
 
-    if (warp == 0) {
+    if (warp < kTcLoadWarps) {
         // Loads.  Stage i of this CTA = K block i % n_stages of its tile
-        // number i / n_stages; ring position i % kTcStages.
-        const int first = min(kTcStages, total_stages);
-        int tile = blockIdx.x, st = 0;
-        TcTile tt = tc_tile(tile, nblk, tblk);
-        for (int i = 0; i < first; i++) {  // constant weights: before the dependency wait
-            if (lane == 2 * i) {
-                mbar_arrive_expect_tx(&s.full[i], kStageBytes);
-                tma_load_3d(s.w[i], &map_w, st * kTcBlockK, tt.n0, tt.bz, &s.full[i]);
+        // number i / n_stages, ring position i % kTcStages; warp i % 2 issues
+        // it.  The first kTcStages stages: lane 2r loads stage r's weights
+        // (before the dependency wait), lane 2r + 1 its activations.
+        {
+            const int r = lane >> 1;
+            const bool mine = r < min(kTcStages, total_stages) && r % kTcLoadWarps == warp;
+            const int lt0 = r / n_stages, st0 = r - lt0 * n_stages;
+            const TcTile t0 = tc_tile(blockIdx.x + lt0 * gridDim.x, nblk, tblk);
+            if (mine && !(lane & 1)) {
+                mbar_arrive_expect_tx(&s.full[r], kStageBytes);
+                tma_load_3d(s.w[r], &map_w, st0 * kTcBlockK, t0.n0, t0.bz, &s.full[r]);
             }
-            if (++st == n_stages) st = 0, tile += gridDim.x, tt = tc_tile(tile, nblk, tblk);
+            __syncwarp();
+            pdl_wait();
+            pdl_trigger();
+            if (mine && (lane & 1)) tma_load_3d(s.x[r], &map_x, st0 * kTcBlockK, t0.tb * BT, 0, &s.full[r]);
+            __syncwarp();
         }
-        __syncwarp();
-        pdl_wait();
-        pdl_trigger();
-        tile = blockIdx.x, st = 0;
-        tt = tc_tile(tile, nblk, tblk);
-        for (int i = 0; i < total_stages && !s.abort; i++) {
+        int i = kTcStages + warp, tile = blockIdx.x, st = i;
+        while (st >= n_stages) st -= n_stages, tile += gridDim.x;
+        TcTile tt = tc_tile(tile, nblk, tblk);
+        for (; i < total_stages && !s.abort; i += kTcLoadWarps) {
             const int r = i % kTcStages;
-            const bool refill = i >= kTcStages;
-            if (refill) {
-                if (!tc_wait(s, &s.empty[r], ((i / kTcStages) - 1) & 1)) break;
-                if (lane == 2 * r) mbar_arrive_expect_tx(&s.full[r], kStageBytes);
-                __syncwarp();
-            }
-            const bool wl = refill && lane == 2 * r, xl = lane == 2 * r + 1;
+            if (!tc_wait(s, &s.empty[r], ((i / kTcStages) - 1) & 1)) break;
+            if (lane == 2 * r) mbar_arrive_expect_tx(&s.full[r], kStageBytes);
+            __syncwarp();
+            const bool wl = lane == 2 * r, xl = lane == 2 * r + 1;
             if (wl || xl)
                 tma_load_3d(wl ? (void *)s.w[r] : (void *)s.x[r], wl ? &map_w : &map_x, st * kTcBlockK,
                             wl ? tt.n0 : tt.tb * BT, wl ? tt.bz : 0, &s.full[r]);
             __syncwarp();
-            if (++st == n_stages) st = 0, tile += gridDim.x, tt = tc_tile(tile, nblk, tblk);
+            st += kTcLoadWarps;
+            if (st >= n_stages) {
+                while (st >= n_stages) st -= n_stages, tile += gridDim.x;
+                tt = tc_tile(tile, nblk, tblk);
+            }
         }
-    } else if (warp <= kTcMmaWarps) {
-        // MMA: warp 1 + w takes stages w, w + kTcMmaWarps, ...; lane j < 4
-        // issues group j of the stage and commits it.
+    } else if (warp < kTcEpiWarp0) {
+        // MMA: warp kTcLoadWarps + w takes stages w, w + kTcMmaWarps, ...;
+        // lane j < 4 issues group j of the stage and commits it.
         const uint32_t idesc = idesc_i8(kTcBlockN, BT);
-        int lt = 0, st = warp - 1;  // stage i = lt * n_stages + st
+        const int mw = warp - kTcLoadWarps;
+        int lt = 0, st = mw;  // stage i = lt * n_stages + st
         while (st >= n_stages) st -= n_stages, lt++;
-        for (int i = warp - 1; i < total_stages && !s.abort; i += kTcMmaWarps) {
+        for (int i = mw; i < total_stages && !s.abort; i += kTcMmaWarps) {
             const int r = i % kTcStages;
             if (!tc_wait(s, &s.full[r], (i / kTcStages) & 1)) break;
             const int groups = min(4, G - 4 * st);
@@ -236,31 +240,25 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     } else {
         // Epilogue.  Loads run one group ahead of the arithmetic; groups go
         // in pairs (even: dA, odd: dB; G is even) inside 8-group scale chunks,
-        // so buffers, scale halves and slot boundaries are fixed at compile time.
+        // so buffers, scale halves and slot boundaries are fixed at compile
+        // time (Q divides 8, so group g sits at slot position (g % 8) % Q).
         const int quad = warp & 3, c0 = ((warp - kTcEpiWarp0) >> 2) * EC;
         const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)c0;
         const bool vec = p.sw_vec != 0;
-        const uint64_t neg_magic = f2_pack(-12582912.0f, -12582912.0f);
         pdl_wait();
         pdl_trigger();
-        uint32_t lsq = 0xFFFFFFFFu;  // TMEM slot sequence of the latest load
-        // load group g (slot position g % Q); a slot's first group waits for its MMAs
-        auto load_group = [&](int g, uint32_t(&d)[EC]) -> bool {
-            if (g % Q == 0) {
-                lsq++;
-                if (!tc_wait(s, &s.acc_full[lsq % S], (lsq / S) & 1)) return false;
-                tc_fence_after();
-            }
-            tmem_ld<EC>(lane_base + (lsq % S) * Sh::kSlotCols + (uint32_t)((g % Q) * BT), d);
+        uint32_t lsq = 0xFFFFFFFFu, slot_addr = 0;  // TMEM slot of the latest load
+        auto next_slot = [&]() -> bool {  // wait for the next slot's MMAs
+            lsq++;
+            if (!tc_wait(s, &s.acc_full[lsq % S], (lsq / S) & 1)) return false;
+            tc_fence_after();
+            slot_addr = lane_base + (lsq % S) * Sh::kSlotCols;
             return true;
         };
-        // after the wait for group g's load: release its slot if g was the slot's last group
-        auto release = [&](int g) {
-            if (g % Q == Q - 1 || g == G - 1) {
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&s.acc_empty[lsq % S]);
-            }
+        auto release_slot = [&]() {  // the latest slot is in registers
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&s.acc_empty[lsq % S]);
         };
         auto scale_row = [&](int tile) {
             const TcTile tn = tc_tile(tile, nblk, tblk);
@@ -272,10 +270,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         bool ok = my_tiles > 0;
         if (ok) {
             sc_nx = tc_scales8(scale_row(blockIdx.x), 0, G, vec);
-            ok = load_group(0, dA);
+            ok = next_slot();
             if (ok) {
+                tmem_ld<EC>(slot_addr, dA);
                 tmem_ld_wait(dA);
-                release(0);
             }
         }
         for (int lt = 0; lt < my_tiles && ok; lt++) {
@@ -301,7 +299,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 if (special) scale = half_to_float_ref_fast(h);
                 const uint64_t s2 = f2_pack(scale, scale);
 #pragma unroll
-                for (int c = 0; c < EC / 2; c++) tc_fold2(acc[c], d[2 * c], d[2 * c + 1], s2, neg_magic);
+                for (int c = 0; c < EC / 2; c++) tc_fold2(acc[c], d[2 * c], d[2 * c + 1], s2);
                 if constexpr (kAccOut) {  // int32 accumulators of every group (parity checks)
                     if (nv) {
 #pragma unroll
@@ -319,22 +317,23 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 for (int gi = 0; gi < 8; gi += 2) {
                     const int g = c8 + gi;
                     if (g >= G) break;
-                    // group g is in dA; g + 1 (G is even) loads into dB meanwhile
-                    ok = load_group(g + 1, dB);
+                    // group g is in dA; g + 1 (same slot: its position is odd) loads into dB
+                    tmem_ld<EC>(slot_addr + (uint32_t)(((gi + 1) % Q) * BT), dB);
                     fold(dA, sc, gi, special, g);
-                    if (!ok) break;
                     tmem_ld_wait(dB);
-                    release(g + 1);
-                    // g + 1 is in dB; next into dA: g + 2, or the next tile's group 0
+                    // g + 1 ends its slot at an even boundary or at the tile's end
                     const bool last = g + 2 >= G;
+                    const bool slot_end = (gi + 2) % Q == 0 || last;
+                    if (slot_end) release_slot();
+                    // next into dA: g + 2, or the next tile's group 0
                     const bool next = !last || more_tiles;
-                    if (next) ok = load_group(last ? 0 : g + 2, dA);
+                    if (next) {
+                        if (slot_end) ok = next_slot();
+                        if (ok) tmem_ld<EC>(slot_addr + (uint32_t)(last ? 0 : ((gi + 2) % Q) * BT), dA);
+                    }
                     fold(dB, sc, gi + 1, special, g + 1);
                     if (!ok) break;
-                    if (next) {
-                        tmem_ld_wait(dA);
-                        release(last ? 0 : g + 2);
-                    }
+                    if (next) tmem_ld_wait(dA);
                 }
             }
             if (!ok) break;
@@ -434,7 +433,7 @@ static int launch_bt(const MatmulArgs &a, const TcParams &p, cudaStream_t stream
 
 template <int BT>
 static int launch_bt(const MatmulArgs &a, const TcParams &p, cudaStream_t stream) {
-    if constexpr (BT == 64) {
+    if constexpr (BT == 64) {  // no residual: its 32 registers do not fit beside 64-token tiles
         return a.acc ? launch_bt<64, true, false>(a, p, stream) : launch_bt<64, false, false>(a, p, stream);
     } else {
         if (a.acc) return a.residual ? launch_bt<BT, true, true>(a, p, stream) : launch_bt<BT, true, false>(a, p, stream);
@@ -470,7 +469,6 @@ int launch_gemm_i8g32_tc(const MatmulArgs &a, cudaStream_t stream) {
     TcParams p{a.m,     a.n, a.k,        a.ldy, a.batch,    a.sa, a.sw, a.sw_stride, a.y_stride, a.y, a.residual,
                a.acc, a.status, sw_vec ? 1 : 0};
     switch (pick_bt(a)) {
-        // a residual's registers do not fit beside 64-token tiles
         case 64: return a.residual ? launch_bt<32>(a, p, stream) : launch_bt<64>(a, p, stream);
         case 32: return launch_bt<32>(a, p, stream);
         default: return launch_bt<16>(a, p, stream);

@@ -122,7 +122,8 @@ template <int N>
 __device__ __forceinline__ void tmem_ld(uint32_t taddr, uint32_t (&r)[N]) {
     if constexpr (N == 4) tmem_ld4(taddr, r);
     else if constexpr (N == 8) tmem_ld8(taddr, r);
-    else tmem_ld16(taddr, r);
+    else if constexpr (N == 16) tmem_ld16(taddr, r);
+    else tmem_ld32(taddr, r);
 }
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 // Waits for this thread's TMEM loads and ties the destination registers to
