@@ -220,12 +220,15 @@ class DecodeWorkload:
 
     cfg5 (default): 1024 independent sessions per GPU (global sessions
     round-robin over ranks), KV lengths U[64,1024], two packed 512-row
-    batches per step.  cfg2: 64 sessions, KV lengths U[16,512], one batch.
-    One step = one decoded token for every session on this GPU: for each
-    batch, ndl_forward_batch + masked/greedy argmax, the ids fed back as the
-    next step's tokens.  value counts the device time of the batches
-    (CUDA events on the engine stream); e2e also counts the host round trip
-    of the token ids between batches."""
+    batches per step.  Each batch is its own engine (512 sessions, its own
+    stream and KV pool), so the two batches of a step are in flight together
+    and one fills the other's latency-bound phases.  cfg2: 64 sessions, KV
+    lengths U[16,512], one batch.  One step = one decoded token for every
+    session on this GPU: every batch's ndl_forward_batch is issued, then each
+    batch's masked/greedy argmax, the ids fed back as the next step's tokens.
+    value counts the device time of the steps (CUDA events from before the
+    first batch's launch to after the last batch's ids, every stream joined);
+    e2e also counts the host time between steps."""
 
     PRESETS = {
         "cfg5": dict(sessions=1024, batch_rows=512, lo=64, hi=1024, seed=5, name="cfg5_dp_decode"),
@@ -258,35 +261,53 @@ class DecodeWorkload:
 
         eng_mod, model = self.model()
         cap = ((self.hi + self.extra_steps + 63) // 64) * 64
-        self.engine = eng_mod.BatchedEngine(model, slots=self.sessions, context_length=cap,
-                                            chunk_size=self.batch_rows, max_heads=self.batch_rows,
-                                            device=device.index or 0)
         self.gids, self.lengths, self.tokens = self.global_layout(rank, world)
-        for j in range(self.sessions):
-            self.engine.fill_synthetic(j, int(self.lengths[j]), self.seed, int(self.gids[j]))
-        self.stream = torch.cuda.ExternalStream(self.engine.stream())
+        # batch b = sessions [b * batch_rows, ...) on engine b, slots 0..
         self.batches = [np.arange(b, min(b + self.batch_rows, self.sessions), dtype=np.int32)
                         for b in range(0, self.sessions, self.batch_rows)]
+        self.engines = []
+        for rows in self.batches:
+            eng = eng_mod.BatchedEngine(model, slots=len(rows), context_length=cap, chunk_size=self.batch_rows,
+                                        max_heads=self.batch_rows, device=device.index or 0)
+            for j, g in enumerate(rows):
+                eng.fill_synthetic(j, int(self.lengths[g]), self.seed, int(self.gids[g]))
+            self.engines.append(eng)
+        self.engine = self.engines[0]
+        self.streams = [torch.cuda.ExternalStream(e.stream()) for e in self.engines]
+        self.stream = self.streams[0]
+        self.slots = [np.arange(len(rows), dtype=np.int32) for rows in self.batches]
         self.attn_bytes = 0
         self.spans = []
         self.launches_per_batch = 0
         torch.cuda.synchronize()
 
-    def step(self, timed=False):
+    def step(self, timed=False, overlap=True):
+        """overlap=False runs the batches one after another (the per-kernel
+        profiling pass, so that each kernel's time is its own)."""
         import torch
 
-        heads = [np.arange(len(b), dtype=np.int32) for b in self.batches]
         launches = 0
+        if not overlap:
+            for b, rows in enumerate(self.batches):
+                self.engines[b].forward_batch(self.tokens[rows], self.slots[b], self.slots[b])
+                ids = self.engines[b].sample_argmax()
+                if timed:
+                    pos = self.lengths[rows] + 1
+                    self.attn_bytes += 12 * (int(pos.sum()) * 8 * 136 + len(rows) * 8 * (64 + 4 + 256))
+                self.lengths[rows] += 1
+                self.tokens[rows] = ids
+            return 0
+        if timed:
+            ev0 = torch.cuda.Event(enable_timing=True)
+            ev1 = torch.cuda.Event(enable_timing=True)
+            ev0.record(self.streams[0])
+            for st in self.streams[1:]:
+                st.wait_event(ev0)
         for b, rows in enumerate(self.batches):
+            self.engines[b].forward_batch(self.tokens[rows], self.slots[b], self.slots[b])
+        for b, rows in enumerate(self.batches):
+            ids = self.engines[b].sample_argmax()
             if timed:
-                ev0 = torch.cuda.Event(enable_timing=True)
-                ev1 = torch.cuda.Event(enable_timing=True)
-                ev0.record(self.stream)
-            self.engine.forward_batch(self.tokens[rows], rows, heads[b])
-            ids = self.engine.sample_argmax()
-            if timed:
-                ev1.record(self.stream)
-                self.spans.append((ev0, ev1))
                 # algorithmic attention bytes: K+V int8 + 2 fp32 scales per position and head,
                 # plus q, q scale and the fp32 output per (row, head)
                 pos = self.lengths[rows] + 1
@@ -294,6 +315,13 @@ class DecodeWorkload:
             self.lengths[rows] += 1
             self.tokens[rows] = ids
             launches += 1 + 12 * 10 + 3 + 1
+        if timed:
+            for st in self.streams[1:]:
+                done = torch.cuda.Event()
+                done.record(st)
+                self.streams[0].wait_event(done)
+            ev1.record(self.streams[0])
+            self.spans.append((ev0, ev1))
         return launches
 
     def units_per_step(self):
@@ -684,10 +712,11 @@ def run_decode(args, rank, world, local):
     torch.cuda.set_device(device)
     wl = make_workload(args.workload, args)
     wl.setup(device, rank, world)
-    eng = wl.engine
+    engines = wl.engines
     for _ in range(args.warmup):
         wl.step()
-    eng.sync()
+    for e in engines:
+        e.sync()
     barrier(world)
     torch.cuda.synchronize()
     launches = 0
@@ -699,7 +728,8 @@ def run_decode(args, rank, world, local):
             launches += wl.step(timed=True)
         t_end.record(wl.stream)
         torch.cuda.synchronize()
-    eng.sync()
+    for e in engines:
+        e.sync()
     barrier(world)
     # second pass, same work: per-kernel-class CUDA events for the roofline and
     # the time shares (kept out of the headline timing above)
@@ -708,13 +738,18 @@ def run_decode(args, rank, world, local):
     wl.attn_bytes = 0
     spans_main = wl.spans
     wl.spans = []
-    eng.profile(True)
-    eng.profile_read(reset=True)
+    for e in engines:
+        e.profile(True)
+        e.profile_read(reset=True)
     for _ in range(prof_steps):
-        wl.step(timed=True)
-    eng.sync()
-    prof = eng.profile_read(reset=True)
-    eng.profile(False)
+        wl.step(timed=True, overlap=False)
+    prof = {}
+    for e in engines:
+        e.sync()
+        for k, (ms, n) in e.profile_read(reset=True).items():
+            pm, pn = prof.get(k, (0.0, 0))
+            prof[k] = (pm + ms, pn + n)
+        e.profile(False)
     prof_attn_bytes = wl.attn_bytes
     wl.attn_bytes, wl.spans = attn_bytes_main, spans_main
     dev_ms = max_over_ranks(wl.device_ms(), world)
@@ -757,7 +792,8 @@ def run_decode(args, rank, world, local):
         line["cpu_baseline"] = {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample}
     if rank == 0:
         print(json.dumps(line), flush=True)
-    eng.close()
+    for e in engines:
+        e.close()
 
 
 def run_ours(args, rank, world, local):
