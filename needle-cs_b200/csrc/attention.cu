@@ -491,6 +491,55 @@ __global__ void __launch_bounds__(256) attn_merge_kernel(AttnArgs a) {
     *reinterpret_cast<float2 *>(a.out + (size_t)w * kHeadDim + 2 * lane) = make_float2(m0 * inv, m1 * inv);
 }
 
+// attn_merge_kernel fused with the per-row quantize of the attention
+// output (the o-projection's input), bit-identical to the two launches:
+// CTA per row, warp per head; a head of a one-chunk row is read back from
+// out.  The row peak (exact max of |x| over heads x 64) goes through shared
+// memory; scale, inverse and rounding as Scalar.QuantizeInt8
+// (src/Needle/Scalar.cs:67-74).
+__global__ void __launch_bounds__(1024) attn_merge_quantize_kernel(AttnArgs a) {
+    pdl_enter();
+    __shared__ float head_peak[32];
+    const int row = blockIdx.x, head = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int w = row * a.heads + head;
+    const int len = a.row_pos[row] + 1;
+    const bool valid = len >= 1 && len <= a.max_pages * kPagePositions;
+    const int pages = (len + kPagePositions - 1) / kPagePositions;
+    const int n_chunks = valid ? (pages + a.chunk_pages - 1) / a.chunk_pages : 1;
+    float2 *o = reinterpret_cast<float2 *>(a.out + (size_t)w * kHeadDim + 2 * lane);
+    float2 v;
+    if (n_chunks >= 2) {
+        const float *parts = a.partials + (size_t)w * a.max_chunks * kPartialFloats;
+        float peak = -INFINITY;
+        for (int c = 0; c < n_chunks; c++) peak = fmaxf(peak, parts[c * kPartialFloats + 64]);
+        float total = 0.0f, m0 = 0.0f, m1 = 0.0f;
+        for (int c = 0; c < n_chunks; c++) {
+            const float *pc = parts + c * kPartialFloats;
+            const float wgt = expf(pc[64] - peak);
+            total += wgt * pc[65];
+            const float2 pv = *reinterpret_cast<const float2 *>(pc + 2 * lane);
+            m0 += wgt * pv.x;
+            m1 += wgt * pv.y;
+        }
+        const float inv = 1.0f / total;
+        v = make_float2(m0 * inv, m1 * inv);
+        *o = v;
+    } else {
+        v = *o;
+    }
+    const float hp = warp_max_f(fmaxf(fabsf(v.x), fabsf(v.y)));
+    if (lane == 0) head_peak[head] = hp;
+    __syncthreads();
+    float peak = 0.0f;
+    for (int h = 0; h < a.heads; h++) peak = fmaxf(peak, head_peak[h]);
+    const float scale = peak > 0.0f ? __fdiv_rn(peak, 127.0f) : 1.0f;
+    const float inverse = __fdiv_rn(1.0f, scale);
+    const uint32_t b0 = (uint8_t)quant1(v.x, inverse), b1 = (uint8_t)quant1(v.y, inverse);
+    reinterpret_cast<uint16_t *>(a.q_out + (size_t)row * a.heads * kHeadDim)[head * 32 + lane] =
+        (uint16_t)(b0 | (b1 << 8));
+    if (threadIdx.x == 0) a.s_out[row] = scale;
+}
+
 int launch_attn_decode(const AttnArgs &a, cudaStream_t stream) {
     if (a.rows == 0) return NDL_OK;
     static bool configured = false;  // per process; the attribute is per device function
@@ -511,7 +560,13 @@ int launch_attn_decode(const AttnArgs &a, cudaStream_t stream) {
     if (blocks > resident) blocks = resident;
     launch_kernel(attn_decode_kernel, dim3((unsigned)blocks), dim3(kAttnWarps * 32), smem, stream, a);
     int st = check_launch("attn_decode");
-    if (st != NDL_OK || a.max_chunks < 2) return st;
+    if (st != NDL_OK) return st;
+    if (a.q_out) {
+        if (a.heads > 32) return set_error(NDL_ERR_INVALID_ARG, "attention: %d heads > 32", a.heads);
+        launch_kernel(attn_merge_quantize_kernel, dim3(a.rows), dim3(a.heads * 32), 0, stream, a);
+        return check_launch("attn_merge_quantize");
+    }
+    if (a.max_chunks < 2) return st;
     const int warps = a.rows * a.heads;
     launch_kernel(attn_merge_kernel, dim3((warps + 7) / 8), dim3(256), 0, stream, a);
     return check_launch("attn_merge");

@@ -422,12 +422,8 @@ int step_kernels(ndl_engine *e, int rows, int heads) {
             AttnArgs aa{e->q8, e->qs, d_slot, d_pos, d_order, e->d_page_table, e->max_pages, e->pool,
                         (long long)e->page_bytes, e->ec.kv_pages, l, c.heads, rows, chunk_pages, max_chunks,
                         1.0f / sqrtf((float)c.head_dim), e->attn, e->partials, e->arrivals, e->d_status,
-                        e->ec.slots};
-            TRY(launch_attn_decode(aa, s));
-        }
-        {
-            ProfScope p(e, NDL_PROF_NORM_QUANT);
-            TRY(launch_quantize_rows(e->attn, nullptr, rows, d, e->qa, e->sa, s));
+                        e->ec.slots, e->qa, e->sa};
+            TRY(launch_attn_decode(aa, s));  // merge + quantize of the output into qa, sa
         }
         {
             ProfScope p(e, NDL_PROF_GEMM_O);
@@ -443,9 +439,8 @@ int step_kernels(ndl_engine *e, int rows, int heads) {
             AttnArgs ca{e->q8, e->qs, d_cslot, d_cpos, d_order, e->d_page_table, e->max_pages, e->pool,
                         (long long)e->page_bytes, e->ec.kv_pages, l, c.heads, rows, chunk_pages, max_chunks,
                         1.0f / sqrtf((float)c.head_dim), e->attn, e->partials, e->arrivals, e->d_status,
-                        e->ec.slots};
+                        e->ec.slots, e->qa, e->sa};
             TRY(launch_attn_decode(ca, s));
-            TRY(launch_quantize_rows(e->attn, nullptr, rows, d, e->qa, e->sa, s));
             TRY(ndl_matmul_i8g32(e->qa, e->sa, rows, L.w_co, L.s_co, d, d, e->x, d, e->x, nullptr, s));
         }
         {

@@ -70,6 +70,10 @@ struct AttnArgs {
     int *arrivals;    // unused (kept for layout stability)
     int *status;
     int slots;        // rows of page_table (bounds check)
+    // nullable: the row's heads x 64 outputs quantized per row
+    // (Scalar.QuantizeInt8), the o-projection's input, in the merge launch
+    int8_t *q_out;    // [rows][heads * 64]
+    float *s_out;     // [rows]
 };
 int launch_attn_decode(const AttnArgs &a, cudaStream_t stream);
 
