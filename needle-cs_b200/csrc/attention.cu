@@ -7,16 +7,17 @@
 //
 // Decode attention (Scalar.AttentionHead src/Needle/Scalar.cs:290-312,
 // AttentionBatch.ExecuteChunk + MergePartials src/Needle/Blocks.cs:750-990):
-// persistent warps stream (row, head, chunk of pages) items.  Each page's
-// 8704-byte (layer, head) record arrives in shared memory by one
-// cp.async.bulk (2-stage ring per warp, mbarrier completion, bounded waits).  Scores
-// are exact int8 dots (mma.sync s8) scaled by ks * (qs / sqrt(d)); softmax
-// is online (running max, rescaled sum) in fp32 with expf; V is accumulated
-// in fp32 by mma.sync f16 with hi/lo-split probability weights.  A row
-// longer than one chunk (a fixed number of pages, so the split depends only
-// on the row's own length) writes (peak, sum, unnormalised output) partials
-// that attn_merge_kernel combines with exp(peak - max) weights, like
-// MergePartials.
+// persistent warps stream (row, head, chunk of pages) items from a work list
+// built once per step.  Each page's 8704-byte (layer, head) record arrives
+// in shared memory by one cp.async.bulk, issued by a producer warp into a
+// 3-stage ring per consumer warp (mbarrier completion, bounded waits).
+// Scores are exact int8 dots (mma.sync s8) scaled by ks * (qs / sqrt(d));
+// softmax is online (running max, rescaled sum) in fp32 with expf; V is
+// accumulated exactly by mma.sync s8 x u8 over 24-bit fixed-point
+// probability weights.  A row longer than one chunk (a fixed number of
+// pages, so the split depends only on the row's own length) writes (peak,
+// sum, unnormalised output) partials that attn_merge_kernel combines with
+// exp(peak - max) weights, like MergePartials.
 #include <mutex>
 
 #include "common.cuh"
@@ -180,15 +181,18 @@ int launch_cross_kv_write(const float *y, int frames, int heads, const int32_t *
 }
 
 // ------------------------------------------------------ decode attention --
-constexpr int kAttnWarps = 4;
-constexpr int kAttnStages = 2;
-constexpr int kDigitOffset = kAttnStages * kKvBlockBytes + 64;  // after the ring and its barriers
-constexpr int kWarpSmem = kDigitOffset + 256;                     // + PV weight digits [4][64]
+constexpr int kAttnConsumers = 4;  // consumer warps per CTA; warp 4 is the producer
+constexpr int kAttnStages = 3;     // ring stages per consumer
+constexpr int kAttnThreads = 32 * (kAttnConsumers + 1);
+constexpr int kAttnCtasPerSm = 2;  // 2 x 4 consumers x 3 stages x 8.7 KB = 209 KB of ring per SM
+constexpr int kConsumerSmem = kAttnStages * kKvBlockBytes + 256;  // ring + PV weight digits [4][64]
+constexpr int kAttnBarOffset = kAttnConsumers * kConsumerSmem;  // full[c][s], then empty[c][s]
+constexpr int kAttnSmem = kAttnBarOffset + 2 * kAttnConsumers * kAttnStages * 8;
 // int32 PV accumulators gain at most 64 * 255 * 128 per page; flushing to
 // fp32 every 1024 pages keeps them below 2^31.
 constexpr int kHoldPages = 1024;
 constexpr uint32_t kWaitLimit = 1u << 22;
-
+constexpr uint32_t kPollLimit = 1u << 24;  // producer polls without progress (with a short sleep each)
 
 // Work item i = (row in LPT order, head, chunk) with chunk innermost.
 struct AttnItem {
@@ -231,9 +235,62 @@ __device__ __forceinline__ void mma_s8u8_m16n8k32(int (&d)[4], const uint4 &a, u
         : "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w), "r"(b0), "r"(b1));
 }
 
-// Persistent: each warp walks items warp_gid, warp_gid + W, ... and streams
-// their pages through its 2-stage ring without draining between items.
-// Per page (64 positions), all products on int8 tensor cores:
+__device__ __forceinline__ AttnWork attn_work_of(const AttnArgs &a, const AttnItem &it) {
+    AttnWork w;
+    w.row = it.row;
+    w.head_chunk = it.head | (it.chunk << 16);
+    w.len = it.len;
+    w.pages_chunks = it.n_pages | (it.n_chunks << 16);
+#pragma unroll
+    for (int k = 0; k < kAttnMaxChunkPages; k++)
+        w.page[k] = k < it.n_pages ? a.page_table[(size_t)it.slot * a.max_pages + it.first_page + k] : -1;
+    return w;
+}
+
+// The compacted work list: CTA per row position ri of the LPT order.  Its
+// items (head, chunk innermost) start after the items of rows 0..ri-1, so
+// the CTA first sums those rows' chunk counts, then writes its own items
+// with their page ids.
+__global__ void __launch_bounds__(256) attn_work_kernel(AttnArgs a) {
+    pdl_enter();
+    __shared__ int warp_sum[8];
+    const int ri = blockIdx.x;
+    auto chunks_of = [&](int r) -> int {  // 0 for an out-of-range row
+        const int row = a.row_order ? a.row_order[r] : r;
+        const int len = a.row_pos[row] + 1, slot = a.row_slot[row];
+        if (len < 1 || len > a.max_pages * kPagePositions || slot < 0 || slot >= a.slots) return 0;
+        const int pages = (len + kPagePositions - 1) / kPagePositions;
+        return (pages + a.chunk_pages - 1) / a.chunk_pages;
+    };
+    int part = 0;
+    for (int r = threadIdx.x; r < ri; r += blockDim.x) part += chunks_of(r);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+    if ((threadIdx.x & 31) == 0) warp_sum[threadIdx.x >> 5] = part;
+    __syncthreads();
+    int before = 0;
+    for (int w = 0; w < (int)(blockDim.x >> 5); w++) before += warp_sum[w];
+    const int base = a.heads * before;
+    const int nc = chunks_of(ri);
+    const int items = a.heads * nc;
+    AttnItem it;
+    if (nc == 0 && threadIdx.x == 0) attn_item(a, ri * a.heads * a.max_chunks, it);  // records an out-of-range row
+    for (int t = threadIdx.x; t < items; t += blockDim.x) {
+        const int head = t / nc, chunk = t - head * nc;
+        if (attn_item(a, (ri * a.heads + head) * a.max_chunks + chunk, it)) a.work[base + t] = attn_work_of(a, it);
+    }
+    if (ri == a.rows - 1 && threadIdx.x == 0) *a.n_work = base + items;
+}
+
+// Persistent, warp-specialised.  Items of the work list are dealt to the
+// consumer warps of the grid in snake order (round r gives consumer w the
+// item r*W + w for even r, r*W + W-1-w for odd r; rows are sorted longest
+// first).  Lane c of the producer warp feeds consumer c of its CTA: it
+// issues that consumer's page copies (one cp.async.bulk per 8704-byte page
+// record) into the consumer's 3-stage ring as stages free up, so a consumer
+// never waits on a copy's issue; lanes with a free stage issue together.
+// A consumer waits for a page, moves its K and V^T fragments and scales to
+// registers, frees the stage and computes, all products on int8 tensor cores:
 //  * QK: mma.sync m16n8k32 s8, A = K (16 positions x 32 dims), B = the
 //    query in every column: exact int32 dots.  Lane (gid, tig) keeps tile
 //    tig, i.e. positions 16*tig + gid and 16*tig + gid + 8.
@@ -244,85 +301,145 @@ __device__ __forceinline__ void mma_s8u8_m16n8k32(int (&d)[4], const uint4 &a, u
 //    gives exact int32 sums of digit x v, chained across pages in the
 //    accumulator until the softmax rescale changes; the digits recombine
 //    as D0 * 2^16 + D1 * 2^8 + D2 once per item.
-__global__ void __launch_bounds__(kAttnWarps * 32, 3) attn_decode_kernel(AttnArgs a) {
-    pdl_enter();
+// Every wait and the producer's polling are bounded.
+__global__ void __launch_bounds__(kAttnThreads, kAttnCtasPerSm) attn_decode_kernel(AttnArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int gid = lane >> 2, tig = lane & 3;
-    const int W = gridDim.x * kAttnWarps;
-    const int n_items = a.rows * a.heads * a.max_chunks;
-
-    uint8_t *ring = smem + warp * kWarpSmem;
-    uint64_t *bars = reinterpret_cast<uint64_t *>(ring + kAttnStages * kKvBlockBytes);
-    uint8_t *digits = ring + kDigitOffset;  // [digit 0..2, unused zero row][tig][16 bytes]
-    if (lane == 0) {
-        for (int s = 0; s < kAttnStages; s++) mbar_init(&bars[s], 1);
+    const int W = gridDim.x * kAttnConsumers;
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + kAttnBarOffset);  // [consumer][stage]
+    uint64_t *empty = full + kAttnConsumers * kAttnStages;
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kAttnConsumers * kAttnStages; i++) mbar_init(&full[i], 1), mbar_init(&empty[i], 1);
         fence_mbar_init();
     }
+    __syncthreads();
+    pdl_wait();
+    pdl_trigger();
+    const int n_work = *a.n_work;
+    auto item_of = [&](int cw, int round) { return round * W + ((round & 1) ? W - 1 - cw : cw); };
+
+    if (warp == kAttnConsumers) {
+        // ---------------- producer: lane c feeds consumer c ----------------
+        const int c = lane;
+        const int cw = blockIdx.x * kAttnConsumers + c;
+        bool done = c >= kAttnConsumers;
+        int round = 0, k = 0, n_pages = 0, head = 0;
+        int pg[kAttnMaxChunkPages];
+#pragma unroll
+        for (int j = 0; j < kAttnMaxChunkPages; j++) pg[j] = -1;
+        AttnWork nx{};
+        bool nx_ok = false;
+        auto fetch = [&](int r, AttnWork &w) -> bool {  // the item of round r, if any
+            const int i = item_of(cw, r);
+            if ((long long)r * W >= n_work || i >= n_work) return false;
+            w = a.work[i];
+            return true;
+        };
+        if (!done) nx_ok = fetch(0, nx);
+        unsigned issued = 0;
+        uint32_t idle = 0;
+        bool timed_out = false;
+        while (true) {
+            bool send = false;
+            int page = -1, stage = 0;
+            if (!done && k == n_pages) {  // next item: the prefetched one; fetch the one after it
+                if (!nx_ok) {
+                    done = true;
+                } else {
+                    head = nx.head_chunk & 0xFFFF;
+                    n_pages = nx.pages_chunks & 0xFFFF;
+#pragma unroll
+                    for (int j = 0; j < kAttnMaxChunkPages; j++) pg[j] = nx.page[j];
+                    k = 0;
+                    round++;
+                    nx_ok = fetch(round, nx);
+                }
+            }
+            if (!done) {
+                stage = issued % kAttnStages;
+                send = issued < (unsigned)kAttnStages ||
+                       mbar_test_wait(&empty[c * kAttnStages + stage], ((issued / kAttnStages) - 1) & 1);
+                if (send) {
+                    page = pg[0];
+#pragma unroll
+                    for (int j = 0; j + 1 < kAttnMaxChunkPages; j++) pg[j] = pg[j + 1];
+                    k++;
+                }
+            }
+            if (send) {  // lanes with a free stage issue together
+                uint64_t *bar = &full[c * kAttnStages + stage];
+                if (page < 0 || page >= a.num_pages) {
+                    if (a.status) atomicOr(a.status, kStatusBadPage);
+                    mbar_arrive(bar);
+                } else {
+                    const uint8_t *src = a.pool + (size_t)page * a.page_bytes + kv_block_offset(a.layer, head, a.heads);
+                    fence_proxy_async_smem();
+                    mbar_arrive_expect_tx(bar, kKvBlockBytes);
+                    bulk_g2s(smem + c * kConsumerSmem + stage * kKvBlockBytes, src, kKvBlockBytes, bar);
+                }
+                issued++;
+            }
+            const unsigned busy = __ballot_sync(0xffffffffu, !done), moved = __ballot_sync(0xffffffffu, send);
+            if (!busy) break;
+            if (moved) {
+                idle = 0;
+            } else if (++idle > kPollLimit) {
+                timed_out = true;
+                break;
+            } else {
+                __nanosleep(64);
+            }
+        }
+        if (timed_out && lane == 0 && a.status) atomicOr(a.status, kStatusTimeout);
+        // drain: every copy this lane issued lands before the CTA exits (bounded)
+        for (unsigned j = issued > (unsigned)kAttnStages ? issued - kAttnStages : 0u; j < issued; j++)
+            mbar_wait_bounded(&full[c * kAttnStages + j % kAttnStages], (j / kAttnStages) & 1, kWaitLimit);
+        return;
+    }
+
+    // ---------------- consumer warp ----------------
+    const int cw = blockIdx.x * kAttnConsumers + warp;
+    uint8_t *ring = smem + warp * kConsumerSmem;
+    uint8_t *digits = ring + kAttnStages * kKvBlockBytes;  // [digit 0..2, unused zero row][tig][16 bytes]
+    uint64_t *f_bar = full + warp * kAttnStages, *e_bar = empty + warp * kAttnStages;
     reinterpret_cast<uint2 *>(digits)[lane] = make_uint2(0u, 0u);
     __syncwarp();
-
-    // Items are dealt in a snake order over rows sorted longest first: round
-    // r gives warp w the item r*W + w (even r) or r*W + W-1-w (odd r).
-    const int wg = blockIdx.x * kAttnWarps + warp;
-    auto item_of = [&](int round) { return round * W + ((round & 1) ? W - 1 - wg : wg); };
-    // Producer cursor, kept identically by every lane (the producer steps are
-    // warp-collective).  On entering an item, lanes 0..31 fetch the item's
-    // page ids in one load; lane 0 then takes each page id by shuffle, so a
-    // page's copy is not held up by its page-table load.
-    int p_round = -1;
-    AttnItem pit{};
-    int p_page = 0, p_left = 0;
-    int pid = -1;  // page id of page (first_page + lane) of the producer's item
-    unsigned issued = 0;
-    auto advance_producer = [&]() -> bool {
-        while (p_left == 0) {
-            p_round++;
-            if (p_round * W >= n_items) return false;
-            const int i = item_of(p_round);
-            if (i < n_items && attn_item(a, i, pit)) {
-                p_page = pit.first_page;
-                p_left = pit.n_pages;
-                pid = lane < pit.n_pages ? a.page_table[(size_t)pit.slot * a.max_pages + pit.first_page + lane] : -1;
-            }
-        }
-        return true;
+    // item metadata two items ahead, the query one item ahead
+    auto meta_of = [&](int r) {
+        const int i = item_of(cw, r);
+        if ((long long)r * W >= n_work || i >= n_work) return make_int4(-1, 0, 0, 0);
+        return *reinterpret_cast<const int4 *>(a.work + i);
     };
-    auto issue_one = [&]() {  // all lanes; requires p_left > 0
-        uint64_t *bar = &bars[issued % kAttnStages];
-        const int k = p_page - pit.first_page;
-        int page = __shfl_sync(0xffffffffu, pid, k & 31);
-        if (k >= 32) page = a.page_table[(size_t)pit.slot * a.max_pages + p_page];
-        // each stage's copy comes from its own lane: copies issued by one
-        // thread complete one after another
-        if (lane == (int)(issued % kAttnStages)) {
-            if (page < 0 || page >= a.num_pages) {
-                if (a.status) atomicOr(a.status, kStatusBadPage);
-                asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-            } else {
-                const uint8_t *src =
-                    a.pool + (size_t)page * a.page_bytes + kv_block_offset(a.layer, pit.head, a.heads);
-                fence_proxy_async_smem();
-                mbar_arrive_expect_tx(bar, kKvBlockBytes);
-                bulk_g2s(ring + (issued % kAttnStages) * kKvBlockBytes, src, kKvBlockBytes, bar);
-            }
-        }
-        issued++;
-        p_page++;
-        p_left--;
+    auto q_of = [&](int4 m, uint4 &qv, float &qs) {
+        if (m.x < 0) return;
+        const int head = m.y & 0xFFFF;
+        // query (K dim order): chunk tig = words for both k-steps
+        qv = __ldg(reinterpret_cast<const uint4 *>(a.q + ((size_t)m.x * a.heads + head) * kHeadDim) + tig);
+        qs = __ldg(a.qs + (size_t)m.x * a.heads + head);
     };
-    for (int k = 0; k < kAttnStages && advance_producer(); k++) issue_one();
-
+    int4 meta_a = meta_of(0), meta_b = meta_of(1);
+    uint4 q_nx = make_uint4(0u, 0u, 0u, 0u);
+    float qs_nx = 0.0f;
+    q_of(meta_a, q_nx, qs_nx);
     unsigned consumed = 0;
     bool timed_out = false;
-    for (int round = 0; round * W < n_items && !timed_out; round++) {
-        const int item = item_of(round);
+    for (int round = 0; !timed_out; round++) {
+        const int4 meta = meta_a;
+        if (meta.x < 0) break;  // the list ended for this warp
+        meta_a = meta_b;
+        meta_b = meta_of(round + 2);
+        const uint4 qv = q_nx;
+        const float scale = __fmul_rn(qs_nx, a.inv_sqrt_d);
+        q_of(meta_a, q_nx, qs_nx);
         AttnItem it;
-        if (item >= n_items || !attn_item(a, item, it)) continue;
-        // query (K dim order): chunk tig = words for both k-steps
-        const uint4 qv = __ldg(reinterpret_cast<const uint4 *>(a.q + ((size_t)it.row * a.heads + it.head) * kHeadDim) +
-                               tig);
-        const float scale = __fmul_rn(a.qs[(size_t)it.row * a.heads + it.head], a.inv_sqrt_d);
+        it.row = meta.x;
+        it.head = meta.y & 0xFFFF;
+        it.chunk = meta.y >> 16;
+        it.len = meta.z;
+        it.n_pages = meta.w & 0xFFFF;
+        it.n_chunks = meta.w >> 16;
+        it.first_page = it.chunk * a.chunk_pages;
         float m = -INFINITY, l = 0.0f;
         int e_acc = 12;  // power-of-two scale currently applied to the accumulators
         int acc_i[4][4];
@@ -335,25 +452,36 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 3) attn_decode_kernel(AttnArg
         const int p0 = 16 * tig + gid, p1 = p0 + 8;
         for (int pg = 0; pg < it.n_pages; pg++) {
             const int stage = consumed % kAttnStages;
-            if (!mbar_wait_bounded(&bars[stage], (consumed / kAttnStages) & 1, kWaitLimit)) {
+            if (!mbar_wait_bounded(&f_bar[stage], (consumed / kAttnStages) & 1, kWaitLimit)) {
                 timed_out = true;
                 break;
             }
             const uint8_t *blk = ring + stage * kKvBlockBytes;
             const int valid = min(kPagePositions, it.len - (it.first_page + pg) * kPagePositions);
+            // the page into registers (K and V^T fragments, scales); then the
+            // stage goes back to the producer while this warp computes
+            uint4 kf[4][2], vf[4][2];
+#pragma unroll
+            for (int mt = 0; mt < 4; mt++) {
+                kf[mt][0] = *reinterpret_cast<const uint4 *>(blk + mt * 1024 + lane * 16);
+                kf[mt][1] = *reinterpret_cast<const uint4 *>(blk + mt * 1024 + 512 + lane * 16);
+                vf[mt][0] = *reinterpret_cast<const uint4 *>(blk + kVOffset + mt * 1024 + lane * 16);
+                vf[mt][1] = *reinterpret_cast<const uint4 *>(blk + kVOffset + mt * 1024 + 512 + lane * 16);
+            }
+            const float2 ks = *reinterpret_cast<const float2 *>(blk + kKScaleOffset + 8 * lane);
+            const float2 vs = *reinterpret_cast<const float2 *>(blk + kVScaleOffset + 8 * lane);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&e_bar[stage]);
+            consumed++;
             // ---- QK ----
             int dot0 = 0, dot1 = 0;
 #pragma unroll
             for (int mt = 0; mt < 4; mt++) {
-                const uint4 k0 = *reinterpret_cast<const uint4 *>(blk + mt * 1024 + lane * 16);
-                const uint4 k1 = *reinterpret_cast<const uint4 *>(blk + mt * 1024 + 512 + lane * 16);
                 int d[4] = {0, 0, 0, 0};
-                mma_s8s8_m16n8k32(d, k0, qv.x, qv.y);
-                mma_s8s8_m16n8k32(d, k1, qv.z, qv.w);
+                mma_s8s8_m16n8k32(d, kf[mt][0], qv.x, qv.y);
+                mma_s8s8_m16n8k32(d, kf[mt][1], qv.z, qv.w);
                 if (mt == tig) dot0 = d[0], dot1 = d[2];
             }
-            const float2 ks = *reinterpret_cast<const float2 *>(blk + kKScaleOffset + 8 * lane);
-            const float2 vs = *reinterpret_cast<const float2 *>(blk + kVScaleOffset + 8 * lane);
             const float s0 = p0 < valid ? __fmul_rn(__fmul_rn(__int2float_rn(dot0), ks.x), scale) : -INFINITY;
             const float s1 = p1 < valid ? __fmul_rn(__fmul_rn(__int2float_rn(dot1), ks.y), scale) : -INFINITY;
             // one combined warp reduction: the page's score max and V-scale max
@@ -399,17 +527,12 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 3) attn_decode_kernel(AttnArg
             __syncwarp();
             // ---- PV: column n of B is digit n & 3 (digit 3 = the zero row) ----
             const uint4 b = *reinterpret_cast<const uint4 *>(digits + (gid & 3) * 64 + tig * 16);
-            const uint8_t *vt = blk + kVOffset;
 #pragma unroll
             for (int mt = 0; mt < 4; mt++) {
-                const uint4 v0 = *reinterpret_cast<const uint4 *>(vt + mt * 1024 + lane * 16);
-                const uint4 v1 = *reinterpret_cast<const uint4 *>(vt + mt * 1024 + 512 + lane * 16);
-                mma_s8u8_m16n8k32(acc_i[mt], v0, b.x, b.y);
-                mma_s8u8_m16n8k32(acc_i[mt], v1, b.z, b.w);
+                mma_s8u8_m16n8k32(acc_i[mt], vf[mt][0], b.x, b.y);
+                mma_s8u8_m16n8k32(acc_i[mt], vf[mt][1], b.z, b.w);
             }
-            __syncwarp();
-            consumed++;
-            if (advance_producer()) issue_one();
+            __syncwarp();  // the digits are read before the next page rewrites them
         }
         if (timed_out) break;
         l = warp_sum_f(l);
@@ -453,12 +576,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 3) attn_decode_kernel(AttnArg
             part[65] = l;
         }
     }
-    if (timed_out) {
-        if (lane == 0 && a.status) atomicOr(a.status, kStatusTimeout);
-    }
-    // drain: every issued copy must land before the CTA exits (bounded)
-    for (unsigned k = consumed + (timed_out ? 1u : 0u); k < issued; k++)
-        mbar_wait_bounded(&bars[k % kAttnStages], (k / kAttnStages) & 1, kWaitLimit);
+    if (timed_out && lane == 0 && a.status) atomicOr(a.status, kStatusTimeout);
 }
 
 // Combines the chunks of every long row (Attention.MergePartials,
@@ -540,13 +658,23 @@ __global__ void __launch_bounds__(1024) attn_merge_quantize_kernel(AttnArgs a) {
     if (threadIdx.x == 0) a.s_out[row] = scale;
 }
 
-int launch_attn_decode(const AttnArgs &a, cudaStream_t stream) {
+int launch_attn_work(const AttnArgs &a, cudaStream_t stream) {
     if (a.rows == 0) return NDL_OK;
+    if (!a.work || !a.n_work) return set_error(NDL_ERR_INVALID_ARG, "attention: no work list");
+    launch_kernel(attn_work_kernel, dim3(a.rows), dim3(256), 0, stream, a);
+    return check_launch("attn_work");
+}
+
+int launch_attn_decode(const AttnArgs &a, cudaStream_t stream, bool build_work) {
+    if (a.rows == 0) return NDL_OK;
+    if (a.chunk_pages < 1 || a.chunk_pages > kAttnMaxChunkPages)
+        return set_error(NDL_ERR_INVALID_ARG, "attention: %d pages per item (1..%d)", a.chunk_pages,
+                         kAttnMaxChunkPages);
     static bool configured = false;  // per process; the attribute is per device function
-    const int smem = kAttnWarps * kWarpSmem;
     static int sms = 0;
     if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        cudaError_t e = cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             kAttnSmem);
         if (e != cudaSuccess) return set_error(NDL_ERR_CUDA, "attention smem attribute: %s", cudaGetErrorString(e));
         int dev = 0;
         cudaGetDevice(&dev);
@@ -555,10 +683,14 @@ int launch_attn_decode(const AttnArgs &a, cudaStream_t stream) {
     }
     const long long items = (long long)a.rows * a.heads * a.max_chunks;
     if (items > 0x7FFFFFFF) return set_error(NDL_ERR_INVALID_ARG, "attention: too many work items");
-    long long blocks = (items + kAttnWarps - 1) / kAttnWarps;
-    const long long resident = (long long)sms * 3;  // three CTAs (12 warps) per SM fit the shared memory
+    if (build_work) {
+        int st = launch_attn_work(a, stream);
+        if (st != NDL_OK) return st;
+    }
+    long long blocks = (items + kAttnConsumers - 1) / kAttnConsumers;
+    const long long resident = (long long)sms * kAttnCtasPerSm;  // the CTAs that fit the shared memory
     if (blocks > resident) blocks = resident;
-    launch_kernel(attn_decode_kernel, dim3((unsigned)blocks), dim3(kAttnWarps * 32), smem, stream, a);
+    launch_kernel(attn_decode_kernel, dim3((unsigned)blocks), dim3(kAttnThreads), kAttnSmem, stream, a);
     int st = check_launch("attn_decode");
     if (st != NDL_OK) return st;
     if (a.q_out) {
@@ -578,10 +710,27 @@ using namespace ndl;
 
 static constexpr int kAbiChunkPages = 8;
 
+// Workspace: the chunk partials [rows][heads][chunks][kPartialFloats] fp32,
+// then the work list [rows * heads * chunks] and its length.
+static size_t abi_partial_bytes(int rows, int heads, int max_pages) {
+    const size_t chunks = (size_t)(max_pages + kAbiChunkPages - 1) / kAbiChunkPages;
+    return ((size_t)rows * heads * chunks * kPartialFloats * sizeof(float) + 15) / 16 * 16;
+}
+
 extern "C" NDL_API size_t ndl_attention_paged_workspace(int rows, int heads, int max_pages) {
     if (rows <= 0 || heads <= 0 || max_pages <= 0) return 0;
     const size_t chunks = (size_t)(max_pages + kAbiChunkPages - 1) / kAbiChunkPages;
-    return (size_t)rows * heads * chunks * kPartialFloats * sizeof(float);
+    return abi_partial_bytes(rows, heads, max_pages) + (size_t)rows * heads * chunks * sizeof(AttnWork) + 16;
+}
+
+// Points a.partials, a.work and a.n_work into a workspace of that layout.
+static void abi_carve(AttnArgs &a, void *ws, int rows, int heads, int max_pages) {
+    uint8_t *base = static_cast<uint8_t *>(ws);
+    const size_t pb = abi_partial_bytes(rows, heads, max_pages);
+    const size_t chunks = (size_t)(max_pages + kAbiChunkPages - 1) / kAbiChunkPages;
+    a.partials = reinterpret_cast<float *>(base);
+    a.work = reinterpret_cast<AttnWork *>(base + pb);
+    a.n_work = reinterpret_cast<int *>(base + pb + (size_t)rows * heads * chunks * sizeof(AttnWork));
 }
 
 extern "C" NDL_API int ndl_attention_paged(const int8_t *q, const float *qs, const int32_t *row_slot,
@@ -607,7 +756,8 @@ extern "C" NDL_API int ndl_attention_paged(const int8_t *q, const float *qs, con
     }
     AttnArgs a{q, qs, row_slot, row_pos, nullptr, page_table, max_pages, pool, (long long)page_bytes, num_pages,
                layer, heads, rows, kAbiChunkPages, (max_pages + kAbiChunkPages - 1) / kAbiChunkPages,
-               0.125f, out, static_cast<float *>(ws), nullptr, status, slots};
+               0.125f, out, nullptr, nullptr, status, slots};
+    abi_carve(a, ws, rows, heads, max_pages);
     int rc = launch_attn_decode(a, st);
     if (!workspace) cudaFreeAsync(ws, st);
     return rc;
@@ -640,7 +790,7 @@ extern "C" NDL_API int ndl_attention_paged(const int8_t *q, const float *qs, con
 // ---------------------------------------------------------------------------
 namespace {
 
-constexpr size_t kNoAllocScratchBytes = 4u << 20;  // 4 MiB: 512 rows x 8 heads x 3 chunks fits
+constexpr size_t kNoAllocScratchBytes = 4u << 20;  // 4 MiB: 512 rows x 8 heads x 3 chunks (partials + work list) fit
 constexpr int kNoAllocMaxDevices = 64;
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
@@ -690,6 +840,7 @@ extern "C" NDL_API int ndl_attention_paged_noalloc(const int8_t *q, const float 
     if (st != NDL_OK) return st;
     AttnArgs a{q, qs, row_slot, row_pos, nullptr, page_table, max_pages, pool, (long long)page_bytes, num_pages,
                layer, heads, rows, kAbiChunkPages, (max_pages + kAbiChunkPages - 1) / kAbiChunkPages,
-               0.125f, out, static_cast<float *>(scratch), nullptr, status, slots};
+               0.125f, out, nullptr, nullptr, status, slots};
+    abi_carve(a, scratch, rows, heads, max_pages);
     return launch_attn_decode(a, (cudaStream_t)stream);
 }

@@ -93,6 +93,8 @@ struct ndl_engine {
     size_t meta_ints = 0;
     float *partials = nullptr;
     int *arrivals = nullptr;
+    ndl::AttnWork *attn_work = nullptr, *cross_work = nullptr;  // per-step attention work lists
+    int *n_work = nullptr;                                 // their lengths (self, cross)
     int *d_status = nullptr;
     int32_t *d_ids = nullptr;
     float *d_probs = nullptr, *d_logp = nullptr;
@@ -295,6 +297,12 @@ int build_buffers(ndl_engine *e) {
     e->max_chunks_cap = e->max_pages;  // chunk_pages >= 1
     TRY(dalloc(e, &e->partials, (size_t)R * c.heads * e->max_chunks_cap * kPartialFloats));
     TRY(dalloc(e, &e->arrivals, (size_t)R * c.heads));
+    {
+        const size_t items = (size_t)R * c.heads * ((e->max_pages + kAttnChunkPages - 1) / kAttnChunkPages);
+        TRY(dalloc(e, &e->attn_work, items));
+        if (c.cross) TRY(dalloc(e, &e->cross_work, items));
+        TRY(dalloc(e, &e->n_work, 2));
+    }
     NDL_CUDA(cudaMemsetAsync(e->arrivals, 0, (size_t)R * c.heads * sizeof(int), e->stream));
     TRY(dalloc(e, &e->d_status, 1));
     NDL_CUDA(cudaMemsetAsync(e->d_status, 0, sizeof(int), e->stream));
@@ -398,6 +406,22 @@ int step_kernels(ndl_engine *e, int rows, int heads) {
     // chunk bound comes from the capacity so one captured graph fits any step
     const int chunk_pages = kAttnChunkPages;
     const int max_chunks = (e->max_pages + chunk_pages - 1) / chunk_pages;
+    // the work lists (items, page ids) are the same for every layer: built once
+    {
+        ProfScope p(e, NDL_PROF_PREPARE);
+        AttnArgs w{e->q8, e->qs, d_slot, d_pos, d_order, e->d_page_table, e->max_pages, e->pool,
+                   (long long)e->page_bytes, e->ec.kv_pages, 0, c.heads, rows, chunk_pages, max_chunks,
+                   0.0f, e->attn, e->partials, e->arrivals, e->d_status, e->ec.slots, e->qa, e->sa, e->attn_work,
+                   e->n_work};
+        TRY(launch_attn_work(w, s));
+        if (c.cross) {
+            w.row_slot = e->d_meta + e->off_cslot;
+            w.row_pos = e->d_meta + e->off_cpos;
+            w.work = e->cross_work;
+            w.n_work = e->n_work + 1;
+            TRY(launch_attn_work(w, s));
+        }
+    }
 
     const int d = c.dim, F = c.ffn;
     for (int l = 0; l < c.layers; l++) {
@@ -422,8 +446,8 @@ int step_kernels(ndl_engine *e, int rows, int heads) {
             AttnArgs aa{e->q8, e->qs, d_slot, d_pos, d_order, e->d_page_table, e->max_pages, e->pool,
                         (long long)e->page_bytes, e->ec.kv_pages, l, c.heads, rows, chunk_pages, max_chunks,
                         1.0f / sqrtf((float)c.head_dim), e->attn, e->partials, e->arrivals, e->d_status,
-                        e->ec.slots, e->qa, e->sa};
-            TRY(launch_attn_decode(aa, s));  // merge + quantize of the output into qa, sa
+                        e->ec.slots, e->qa, e->sa, e->attn_work, e->n_work};
+            TRY(launch_attn_decode(aa, s, false));  // merge + quantize of the output into qa, sa
         }
         {
             ProfScope p(e, NDL_PROF_GEMM_O);
@@ -439,8 +463,8 @@ int step_kernels(ndl_engine *e, int rows, int heads) {
             AttnArgs ca{e->q8, e->qs, d_cslot, d_cpos, d_order, e->d_page_table, e->max_pages, e->pool,
                         (long long)e->page_bytes, e->ec.kv_pages, l, c.heads, rows, chunk_pages, max_chunks,
                         1.0f / sqrtf((float)c.head_dim), e->attn, e->partials, e->arrivals, e->d_status,
-                        e->ec.slots, e->qa, e->sa};
-            TRY(launch_attn_decode(ca, s));
+                        e->ec.slots, e->qa, e->sa, e->cross_work, e->n_work + 1};
+            TRY(launch_attn_decode(ca, s, false));
             TRY(ndl_matmul_i8g32(e->qa, e->sa, rows, L.w_co, L.s_co, d, d, e->x, d, e->x, nullptr, s));
         }
         {

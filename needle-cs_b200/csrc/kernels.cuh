@@ -53,6 +53,19 @@ int launch_cross_kv_write(const float *y, int frames, int heads, const int32_t *
 
 constexpr int kPartialFloats = 68;  // 64 outputs + peak + sum, padded to 16 bytes
 
+// One attention work item (row, head, chunk of at most 8 pages) with its
+// page ids resolved: the compacted list of a step's items, in the order the
+// attention kernel deals them, built once per step by launch_attn_work.
+struct AttnWork {
+    int row;
+    int head_chunk;    // head | chunk << 16
+    int len;           // attended positions of the row
+    int pages_chunks;  // pages of this chunk | chunks of the row << 16
+    int page[8];
+};
+static_assert(sizeof(AttnWork) == 48, "three 16-byte loads per item");
+constexpr int kAttnMaxChunkPages = 8;
+
 struct AttnArgs {
     const int8_t *q;  // [rows][heads][64]
     const float *qs;  // [rows][heads]
@@ -74,8 +87,14 @@ struct AttnArgs {
     // (Scalar.QuantizeInt8), the o-projection's input, in the merge launch
     int8_t *q_out;    // [rows][heads * 64]
     float *s_out;     // [rows]
+    AttnWork *work;   // [rows * heads * max_chunks] items, compacted
+    int *n_work;      // the list's length
 };
-int launch_attn_decode(const AttnArgs &a, cudaStream_t stream);
+// Builds the compacted work list of a launch shape (one small launch; the
+// engine builds it once per step and reuses it for every layer).
+int launch_attn_work(const AttnArgs &a, cudaStream_t stream);
+// build_work: launch_attn_work first (callers without a prebuilt list).
+int launch_attn_decode(const AttnArgs &a, cudaStream_t stream, bool build_work = true);
 
 // Streaming int8 GEMV (mma.sync m16n8k32 per 32-column group), any m.
 int launch_gemv_i8g32(const MatmulArgs &a, cudaStream_t stream);

@@ -28,9 +28,6 @@ __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, i
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap *map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
-__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
 
 // ---- TMEM ----
 __device__ __forceinline__ void tmem_alloc(uint32_t *dst_smem, uint32_t cols) {
