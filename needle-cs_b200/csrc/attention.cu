@@ -665,7 +665,20 @@ int launch_attn_work(const AttnArgs &a, cudaStream_t stream) {
     return check_launch("attn_work");
 }
 
-int launch_attn_decode(const AttnArgs &a, cudaStream_t stream, bool build_work) {
+int launch_attn_merge(const AttnArgs &a, cudaStream_t stream) {
+    if (a.rows == 0) return NDL_OK;
+    if (a.q_out) {
+        if (a.heads > 32) return set_error(NDL_ERR_INVALID_ARG, "attention: %d heads > 32", a.heads);
+        launch_kernel(attn_merge_quantize_kernel, dim3(a.rows), dim3(a.heads * 32), 0, stream, a);
+        return check_launch("attn_merge_quantize");
+    }
+    if (a.max_chunks < 2) return NDL_OK;
+    const int warps = a.rows * a.heads;
+    launch_kernel(attn_merge_kernel, dim3((warps + 7) / 8), dim3(256), 0, stream, a);
+    return check_launch("attn_merge");
+}
+
+int launch_attn_decode(const AttnArgs &a, cudaStream_t stream, bool build_work, bool merge) {
     if (a.rows == 0) return NDL_OK;
     if (a.chunk_pages < 1 || a.chunk_pages > kAttnMaxChunkPages)
         return set_error(NDL_ERR_INVALID_ARG, "attention: %d pages per item (1..%d)", a.chunk_pages,
@@ -692,16 +705,8 @@ int launch_attn_decode(const AttnArgs &a, cudaStream_t stream, bool build_work) 
     if (blocks > resident) blocks = resident;
     launch_kernel(attn_decode_kernel, dim3((unsigned)blocks), dim3(kAttnThreads), kAttnSmem, stream, a);
     int st = check_launch("attn_decode");
-    if (st != NDL_OK) return st;
-    if (a.q_out) {
-        if (a.heads > 32) return set_error(NDL_ERR_INVALID_ARG, "attention: %d heads > 32", a.heads);
-        launch_kernel(attn_merge_quantize_kernel, dim3(a.rows), dim3(a.heads * 32), 0, stream, a);
-        return check_launch("attn_merge_quantize");
-    }
-    if (a.max_chunks < 2) return st;
-    const int warps = a.rows * a.heads;
-    launch_kernel(attn_merge_kernel, dim3((warps + 7) / 8), dim3(256), 0, stream, a);
-    return check_launch("attn_merge");
+    if (st != NDL_OK || !merge) return st;
+    return launch_attn_merge(a, stream);
 }
 
 }  // namespace ndl

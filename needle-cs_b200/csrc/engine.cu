@@ -441,13 +441,17 @@ int step_kernels(ndl_engine *e, int rows, int heads) {
                            e->q8, e->qs, e->d_status};
             TRY(launch_kv_write(kw, s));
         }
+        const AttnArgs aa{e->q8, e->qs, d_slot, d_pos, d_order, e->d_page_table, e->max_pages, e->pool,
+                          (long long)e->page_bytes, e->ec.kv_pages, l, c.heads, rows, chunk_pages, max_chunks,
+                          1.0f / sqrtf((float)c.head_dim), e->attn, e->partials, e->arrivals, e->d_status,
+                          e->ec.slots, e->qa, e->sa, e->attn_work, e->n_work};
         {
             ProfScope p(e, NDL_PROF_ATTENTION);
-            AttnArgs aa{e->q8, e->qs, d_slot, d_pos, d_order, e->d_page_table, e->max_pages, e->pool,
-                        (long long)e->page_bytes, e->ec.kv_pages, l, c.heads, rows, chunk_pages, max_chunks,
-                        1.0f / sqrtf((float)c.head_dim), e->attn, e->partials, e->arrivals, e->d_status,
-                        e->ec.slots, e->qa, e->sa, e->attn_work, e->n_work};
-            TRY(launch_attn_decode(aa, s, false));  // merge + quantize of the output into qa, sa
+            TRY(launch_attn_decode(aa, s, false, false));
+        }
+        {
+            ProfScope p(e, NDL_PROF_NORM_QUANT);
+            TRY(launch_attn_merge(aa, s));  // merge + quantize of the output into qa, sa
         }
         {
             ProfScope p(e, NDL_PROF_GEMM_O);

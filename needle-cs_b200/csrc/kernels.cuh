@@ -93,8 +93,11 @@ struct AttnArgs {
 // Builds the compacted work list of a launch shape (one small launch; the
 // engine builds it once per step and reuses it for every layer).
 int launch_attn_work(const AttnArgs &a, cudaStream_t stream);
-// build_work: launch_attn_work first (callers without a prebuilt list).
-int launch_attn_decode(const AttnArgs &a, cudaStream_t stream, bool build_work = true);
+// build_work: launch_attn_work first (callers without a prebuilt list);
+// merge: also launch the merge (and quantize, when q_out is set) after it.
+int launch_attn_decode(const AttnArgs &a, cudaStream_t stream, bool build_work = true, bool merge = true);
+// The merge of long rows' chunk partials (+ the per-row quantize into q_out).
+int launch_attn_merge(const AttnArgs &a, cudaStream_t stream);
 
 // Streaming int8 GEMV (mma.sync m16n8k32 per 32-column group), any m.
 int launch_gemv_i8g32(const MatmulArgs &a, cudaStream_t stream);
