@@ -858,7 +858,7 @@ def run_ours(args, rank, world, local):
             "config": wl.describe(),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": None, "peak_source": peak_kind,
-                         "kernel": "gemv_i8g32_kernel"},
+                         "kernel": "gemv_i8g32_reg_kernel<2> (K 512: activations in registers)"},
             "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_call": e_ms},
             "gpu_launches": launches,

@@ -237,6 +237,123 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 5) gemv_i8g32_kernel(MatmulAr
     }
 }
 
+// K <= 512 (kChunks = G / 8 = 1 or 2), vector scales, no int32 output: the
+// warp's whole activation operand (16 rows x K, 4 registers per group) stays
+// in registers, so the only memory traffic is the weight and scale stream
+// and the outputs (5 - kChunks CTAs per SM fit the registers).  Same tile
+// stream, prefetch and arithmetic as above.
+template <int kChunks>
+__global__ void __launch_bounds__(kGemvWarps * 32, 5 - kChunks) gemv_i8g32_reg_kernel(MatmulArgs a) {
+    pdl_enter();
+    constexpr int G = kChunks * kGemvUnroll;
+    const int lane = threadIdx.x & 31;
+    const int gid = lane >> 2, tig = lane & 3;
+    const int W = gridDim.x * kGemvWarps;
+    const int tiles_per = (a.n + 7) / 8;
+    const int tiles = tiles_per * a.batch;
+    const int t0 = blockIdx.y * 16;
+    const int ta = t0 + gid, tb = ta + 8;
+    const bool va = ta < a.m, vb = tb < a.m;
+    int tile = blockIdx.x * kGemvWarps + (threadIdx.x >> 5);
+    if (tile >= tiles) return;
+    // activation fragments of every group: rows ta, tb (rows past m: zeros)
+    uint2 A0[G], A1[G];
+    {
+        const int8_t *qa = a.q + (size_t)(va ? ta : 0) * a.k + 8 * tig;
+        const int8_t *qb = a.q + (size_t)(vb ? tb : 0) * a.k + 8 * tig;
+#pragma unroll
+        for (int g = 0; g < G; g++) {
+            A0[g] = va ? __ldg(reinterpret_cast<const uint2 *>(qa + g * 32)) : make_uint2(0u, 0u);
+            A1[g] = vb ? __ldg(reinterpret_cast<const uint2 *>(qb + g * 32)) : make_uint2(0u, 0u);
+        }
+    }
+    const float sa_a = va ? a.sa[ta] : 0.0f, sa_b = vb ? a.sa[tb] : 0.0f;
+    const uint64_t neg_magic = f2_pack(-12582912.0f, -12582912.0f);
+    struct Tile {
+        const int8_t *wl;
+        const uint16_t *s0p, *s1p;
+        float *y;
+        int nc;
+    };
+    auto make_tile = [&](int t) {
+        Tile r;
+        const int bz = t / tiles_per, tw = t - bz * tiles_per;
+        const int nl = tw * 8 + gid;
+        r.wl = a.w + (long long)bz * a.w_stride + (size_t)(nl < a.n ? nl : 0) * a.k + 8 * tig;
+        r.nc = tw * 8 + 2 * tig;
+        const uint16_t *sw = a.sw + (long long)bz * a.sw_stride;
+        r.s0p = sw + (size_t)(r.nc < a.n ? r.nc : 0) * G;
+        r.s1p = sw + (size_t)(r.nc + 1 < a.n ? r.nc + 1 : 0) * G;
+        r.y = a.y + (long long)bz * a.y_stride;
+        return r;
+    };
+    Tile cur = make_tile(tile);
+    uint2 B[kGemvUnroll];
+#pragma unroll
+    for (int u = 0; u < kGemvUnroll; u++) B[u] = ld_stream_u2(cur.wl + u * 32);
+    uint4 S0 = ld_stream_u4(cur.s0p), S1 = ld_stream_u4(cur.s1p);
+    while (true) {
+        uint64_t acc_a = 0ull, acc_b = 0ull;  // (t=ta: nc, nc+1), (t=tb: nc, nc+1)
+        const int nt = tile + W;
+        Tile nxt = cur;
+        if (nt < tiles) nxt = make_tile(nt);
+#pragma unroll
+        for (int c = 0; c < kChunks; c++) {
+            // the next chunk (this tile's, or the next tile's first) loads meanwhile
+            uint2 Bn[kGemvUnroll];
+            uint4 S0n = make_uint4(0u, 0u, 0u, 0u), S1n = S0n;
+            const bool last = c + 1 == kChunks;
+            if (!last || nt < tiles) {
+                const int8_t *wn = last ? nxt.wl : cur.wl + (c + 1) * 256;
+#pragma unroll
+                for (int u = 0; u < kGemvUnroll; u++) Bn[u] = ld_stream_u2(wn + u * 32);
+                S0n = ld_stream_u4(last ? nxt.s0p : cur.s0p + (c + 1) * kGemvUnroll);
+                S1n = ld_stream_u4(last ? nxt.s1p : cur.s1p + (c + 1) * kGemvUnroll);
+            }
+            const bool special = any_max_exponent(S0) || any_max_exponent(S1);
+#pragma unroll
+            for (int u = 0; u < kGemvUnroll; u++) {
+                const int g = c * kGemvUnroll + u;
+                int d[4];
+                mma_s8_16x8x32(d, A0[g].x, A1[g].x, A0[g].y, A1[g].y, B[u].x, B[u].y);
+                float s0, s1;
+                if (!special) {
+                    s0 = half_plain(half_of(S0, u));
+                    s1 = half_plain(half_of(S1, u));
+                } else {
+                    s0 = half_to_float_ref_fast(half_of(S0, u));
+                    s1 = half_to_float_ref_fast(half_of(S1, u));
+                }
+                // acc = fma(sw, float(D), acc) per (t, n); float(D) exact by the 1.5*2^23 trick
+                const uint64_t sc = f2_pack(s0, s1);
+                acc_a = f2_fma(sc, f2_add(f2_pack(__int_as_float(d[0] + 0x4B400000), __int_as_float(d[1] + 0x4B400000)),
+                                          neg_magic), acc_a);
+                acc_b = f2_fma(sc, f2_add(f2_pack(__int_as_float(d[2] + 0x4B400000), __int_as_float(d[3] + 0x4B400000)),
+                                          neg_magic), acc_b);
+            }
+            S0 = S0n;
+            S1 = S1n;
+#pragma unroll
+            for (int u = 0; u < kGemvUnroll; u++) B[u] = Bn[u];
+        }
+        float v[4];
+        f2_unpack(acc_a, v[0], v[1]);
+        f2_unpack(acc_b, v[2], v[3]);
+        const int nc = cur.nc;
+        auto store = [&](int t, int n, float x) {
+            size_t o = (size_t)t * a.ldy + n;
+            cur.y[o] = a.residual ? __fadd_rn(a.residual[o], x) : x;
+        };
+        if (va && nc < a.n) store(ta, nc, __fmul_rn(v[0], sa_a));
+        if (va && nc + 1 < a.n) store(ta, nc + 1, __fmul_rn(v[1], sa_a));
+        if (vb && nc < a.n) store(tb, nc, __fmul_rn(v[2], sa_b));
+        if (vb && nc + 1 < a.n) store(tb, nc + 1, __fmul_rn(v[3], sa_b));
+        if (nt >= tiles) break;
+        tile = nt;
+        cur = nxt;
+    }
+}
+
 int launch_gemv_i8g32(const MatmulArgs &a, cudaStream_t stream) {
     static int sms = 0;
     if (!sms) {
@@ -260,6 +377,13 @@ int launch_gemv_i8g32(const MatmulArgs &a, cudaStream_t stream) {
     const int smem = 16 * (a.k + 32);
     const bool sm_a = smem <= 48 * 1024;
     const dim3 blk(kGemvWarps * 32);
+    if (!a.acc && scales_vec && (G == 8 || G == 16)) {  // K = 256 or 512: activations in registers
+        const long long want_r = std::max<long long>(1, (long long)sms * (G == 8 ? 4 : 3) / mtiles);  // resident CTAs
+        const dim3 grid_r((unsigned)std::min<long long>((tiles + kGemvWarps - 1) / kGemvWarps, want_r), (unsigned)mtiles, 1);
+        if (G == 8) launch_kernel(gemv_i8g32_reg_kernel<1>, grid_r, blk, 0, stream, a);
+        else launch_kernel(gemv_i8g32_reg_kernel<2>, grid_r, blk, 0, stream, a);
+        return check_launch("gemv_i8g32_reg");
+    }
 #define NDL_GEMV(ACC, FULL, SMA) launch_kernel(gemv_i8g32_kernel<ACC, FULL, SMA>, dim3(grid), dim3(blk), SMA ? smem : 0, stream, a, sv)
     if (a.acc) {
         if (full) { if (sm_a) NDL_GEMV(true, true, true); else NDL_GEMV(true, true, false); }
