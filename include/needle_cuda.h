@@ -313,6 +313,26 @@ NDL_API int ndl_slot_attach_memory(ndl_engine *e, int slot, int memory_slot);
  * (src/Needle/Engine.cs:367-379). */
 NDL_API int ndl_slot_copy(ndl_engine *e, int dst, int src);
 
+/* Primed prefixes (Engine.PrimedPrefixBytes / ExportPrimedPrefix /
+ * ImportPrimedPrefix, src/Needle/Engine.cs:398-464).  The blob holds the
+ * slot's marked prefix (its length at ndl_slot_mark) in the reference's
+ * layout: int32 length, then per layer keys int8 [len][heads*64], values
+ * int8 [len][heads*64], key scales fp32 [len][heads], value scales fp32
+ * [len][heads] (the synthetic decoders keep no recurrent engine state, so
+ * the reference's state section is empty).  Import replaces the slot's cache
+ * and sets its length and mark to the blob's length; a short buffer or blob
+ * and a length beyond the capacity are NDL_ERR_INVALID_ARG. */
+NDL_API int ndl_slot_prefix_bytes(ndl_engine *e, int slot, size_t *bytes);
+NDL_API int ndl_slot_export_prefix(ndl_engine *e, int slot, void *blob, size_t bytes);
+NDL_API int ndl_slot_import_prefix(ndl_engine *e, int slot, const void *blob, size_t bytes);
+/* Prefix sharing: `dst` (reset first) takes `src`'s marked prefix by
+ * reference: whole KV pages are shared, the partial last page is copied, and
+ * a later write into a shared page copies it first (copy on write).  dst's
+ * length and mark become the prefix length. */
+NDL_API int ndl_slot_share_prefix(ndl_engine *e, int dst, int src);
+/* Pool pages not held by any slot. */
+NDL_API int ndl_engine_free_pages(ndl_engine *e, int *free_pages);
+
 /* Beam search over many utterances at once: Whistle.BeamSearch
  * (src/Needle/Whistle.Decode.cs:224-350) for each utterance, every live
  * beam of every utterance in one forward_batch per step.  Utterance u uses

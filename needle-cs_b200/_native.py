@@ -65,6 +65,11 @@ SIGNATURES = {
     "ndl_slot_fill_memory_synthetic": (c_int, [c_void_p, c_int, c_int, c_u64, c_u64]),
     "ndl_slot_attach_memory": (c_int, [c_void_p, c_int, c_int]),
     "ndl_slot_copy": (c_int, [c_void_p, c_int, c_int]),
+    "ndl_slot_prefix_bytes": (c_int, [c_void_p, c_int, ctypes.POINTER(c_size_t)]),
+    "ndl_slot_export_prefix": (c_int, [c_void_p, c_int, c_void_p, c_size_t]),
+    "ndl_slot_import_prefix": (c_int, [c_void_p, c_int, c_void_p, c_size_t]),
+    "ndl_slot_share_prefix": (c_int, [c_void_p, c_int, c_int]),
+    "ndl_engine_free_pages": (c_int, [c_void_p, ctypes.POINTER(c_int)]),
     "ndl_selftest_bounded_wait": (c_int, [c_int]),
     "ndl_kt_quantize_int8": (c_float, [c_void_p, c_int, c_void_p]),
     "ndl_kt_argmax_masked": (c_int, [c_void_p, c_void_p, c_int, c_int]),

@@ -81,6 +81,7 @@ struct ndl_engine {
     int32_t *d_page_table = nullptr;
     std::vector<int32_t> page_table;  // host mirror [slots][max_pages]
     std::vector<int32_t> free_pages;
+    std::vector<int> page_refs;  // slots holding each pool page (shared prefixes hold one page in many)
     std::vector<int> slot_len, slot_mark;
     std::vector<int> cross_slot;  // memory slot attended by each slot's rows (-1: none)
     // step buffers
@@ -321,15 +322,56 @@ int build_buffers(ndl_engine *e) {
     return NDL_OK;
 }
 
+// A pool page for one slot (reference count 1), or -1 when the pool is empty.
+int alloc_page(ndl_engine *e) {
+    if (e->free_pages.empty()) return -1;
+    const int page = e->free_pages.back();
+    e->free_pages.pop_back();
+    e->page_refs[page] = 1;
+    return page;
+}
+// A slot drops its reference; the page returns to the pool with the last one.
+void release_page(ndl_engine *e, int page) {
+    if (--e->page_refs[page] == 0) e->free_pages.push_back(page);
+}
+
 void free_slot_pages(ndl_engine *e, int slot, int keep_pages, std::vector<int32_t> *updates) {
     int32_t *row = e->page_table.data() + (size_t)slot * e->max_pages;
     for (int i = keep_pages; i < e->max_pages; i++) {
         if (row[i] >= 0) {
-            e->free_pages.push_back(row[i]);
+            release_page(e, row[i]);
             row[i] = -1;
             if (updates) updates->insert(updates->end(), {slot, i, -1});
         }
     }
+}
+
+// Makes page index `pg` of `slot` writable by this slot alone: a missing
+// page is allocated; a page another slot also holds (a shared prefix) is
+// copied first (copy on write: the device copy is queued in `copies` as
+// (from, to)).  Returns the page, or -1 when the pool is exhausted; a new
+// entry is recorded in `updates` as (slot, index, page).
+int writable_page(ndl_engine *e, int slot, int pg, std::vector<int32_t> &updates, std::vector<int32_t> &copies) {
+    int32_t &entry = e->page_table[(size_t)slot * e->max_pages + pg];
+    if (entry >= 0 && e->page_refs[entry] == 1) return entry;
+    const int page = alloc_page(e);
+    if (page < 0) return -1;
+    if (entry >= 0) {
+        copies.insert(copies.end(), {entry, page});
+        release_page(e, entry);
+    }
+    entry = page;
+    updates.insert(updates.end(), {slot, pg, page});
+    return page;
+}
+
+// Queues the page copies of writable_page on the engine stream.
+int copy_pages(ndl_engine *e, const std::vector<int32_t> &copies) {
+    for (size_t i = 0; i < copies.size(); i += 2)
+        NDL_CUDA(cudaMemcpyAsync(e->pool + (size_t)copies[i + 1] * e->page_bytes,
+                                 e->pool + (size_t)copies[i] * e->page_bytes, e->page_bytes,
+                                 cudaMemcpyDeviceToDevice, e->stream));
+    return NDL_OK;
 }
 
 int check_status(ndl_engine *e) {
@@ -580,6 +622,7 @@ NDL_API int ndl_engine_create(const ndl_engine_config *ec, const ndl_decoder_con
     cudaMemcpy(e->d_page_table, e->page_table.data(), e->page_table.size() * 4, cudaMemcpyHostToDevice);
     e->free_pages.resize(pages);
     for (int i = 0; i < pages; i++) e->free_pages[i] = pages - 1 - i;  // pop_back yields 0, 1, 2, ...
+    e->page_refs.assign(pages, 0);
     e->slot_len.assign(ec->slots, 0);
     e->slot_mark.assign(ec->slots, 0);
     e->cross_slot.assign(ec->slots, -1);
@@ -714,16 +757,11 @@ NDL_API int ndl_slot_fill_synthetic(ndl_engine *e, int slot, int count, uint64_t
     if (first + count > e->ec.capacity)
         return set_error(NDL_FAIL_CONTEXT_EXHAUSTED, "slot %d: %d + %d exceeds capacity %d", slot, first, count,
                          e->ec.capacity);
-    std::vector<int32_t> updates;
-    int32_t *row = e->page_table.data() + (size_t)slot * e->max_pages;
-    for (int p = first / kPagePositions; p * kPagePositions < first + count; p++) {
-        if (row[p] < 0) {
-            if (e->free_pages.empty()) return set_error(NDL_ERR_PAGES_EXHAUSTED, "KV page pool exhausted");
-            row[p] = e->free_pages.back();
-            e->free_pages.pop_back();
-            updates.insert(updates.end(), {slot, p, row[p]});
-        }
-    }
+    std::vector<int32_t> updates, copies;
+    for (int p = first / kPagePositions; p * kPagePositions < first + count; p++)
+        if (writable_page(e, slot, p, updates, copies) < 0)
+            return set_error(NDL_ERR_PAGES_EXHAUSTED, "KV page pool exhausted");
+    TRY(copy_pages(e, copies));
     TRY(push_page_updates(e, updates));
     TRY(launch_kv_fill(seed, session, e->dc.layers, e->dc.heads, first, count,
                        e->d_page_table + (size_t)slot * e->max_pages, e->pool, (long long)e->page_bytes,
@@ -737,16 +775,11 @@ namespace {
 
 // Pages for positions [first, first + count) of a slot (host mirror + device table).
 int reserve_pages(ndl_engine *e, int slot, int first, int count) {
-    std::vector<int32_t> updates;
-    int32_t *row = e->page_table.data() + (size_t)slot * e->max_pages;
-    for (int p = first / kPagePositions; p * kPagePositions < first + count; p++) {
-        if (row[p] < 0) {
-            if (e->free_pages.empty()) return set_error(NDL_ERR_PAGES_EXHAUSTED, "KV page pool exhausted");
-            row[p] = e->free_pages.back();
-            e->free_pages.pop_back();
-            updates.insert(updates.end(), {slot, p, row[p]});
-        }
-    }
+    std::vector<int32_t> updates, copies;
+    for (int p = first / kPagePositions; p * kPagePositions < first + count; p++)
+        if (writable_page(e, slot, p, updates, copies) < 0)
+            return set_error(NDL_ERR_PAGES_EXHAUSTED, "KV page pool exhausted");
+    TRY(copy_pages(e, copies));
     return push_page_updates(e, updates);
 }
 
@@ -906,22 +939,16 @@ NDL_API int ndl_forward_batch(ndl_engine *e, const int *tokens, const int *row_s
         m[e->off_head + h] = head_rows[h];
     }
     // pages for the new positions; updates region = [count, (slot, index, page)...]
-    int n_updates = 0;
+    // (a page another slot shares is copied first: copy on write)
+    std::vector<int32_t> updates, copies;
+    for (int r = 0; r < rows; r++)
+        if (writable_page(e, m[e->off_slot + r], m[e->off_pos + r] / kPagePositions, updates, copies) < 0)
+            return set_error(NDL_ERR_PAGES_EXHAUSTED, "KV page pool exhausted");
+    const int n_updates = (int)(updates.size() / 3);
     int32_t *upd = m + e->off_updates;
-    for (int r = 0; r < rows; r++) {
-        int slot = m[e->off_slot + r], pg = m[e->off_pos + r] / kPagePositions;
-        int32_t &entry = e->page_table[(size_t)slot * e->max_pages + pg];
-        if (entry < 0) {
-            if (e->free_pages.empty()) return set_error(NDL_ERR_PAGES_EXHAUSTED, "KV page pool exhausted");
-            entry = e->free_pages.back();
-            e->free_pages.pop_back();
-            upd[1 + 3 * n_updates] = slot;
-            upd[2 + 3 * n_updates] = pg;
-            upd[3 + 3 * n_updates] = entry;
-            n_updates++;
-        }
-    }
+    std::copy(updates.begin(), updates.end(), upd + 1);
     upd[0] = n_updates;
+    TRY(copy_pages(e, copies));
     // longest rows first (LPT order for the attention work list)
     std::vector<int> order(rows);
     for (int r = 0; r < rows; r++) order[r] = r;
@@ -1025,6 +1052,111 @@ NDL_API int ndl_engine_get_info(ndl_engine *e, ndl_engine_info *info) {
     NDL_REQUIRE(e && info, "null argument");
     *info = ndl_engine_info{e->ec.slots, e->ec.capacity, e->dc.vocab, e->ec.max_rows, e->ec.max_heads,
                             e->dc.layers, e->dc.dim, e->dc.heads};
+    return NDL_OK;
+}
+
+// Pool pages not held by any slot.
+NDL_API int ndl_engine_free_pages(ndl_engine *e, int *free_pages) {
+    NDL_REQUIRE(e && free_pages, "null argument");
+    *free_pages = (int)e->free_pages.size();
+    return NDL_OK;
+}
+
+// Engine.PrimedPrefixBytes (src/Needle/Engine.cs:398-400): bytes of the blob
+// of the slot's marked prefix (its length at ndl_slot_mark).
+NDL_API int ndl_slot_prefix_bytes(ndl_engine *e, int slot, size_t *bytes) {
+    NDL_REQUIRE(e && bytes, "null argument");
+    TRY(check_slot(e, slot));
+    *bytes = prefix_blob_bytes(e->dc.layers, e->dc.heads, e->slot_mark[slot]);
+    return NDL_OK;
+}
+
+// Engine.ExportPrimedPrefix (src/Needle/Engine.cs:402-427): the slot's
+// marked prefix as a blob (layout in prefix.cu).
+NDL_API int ndl_slot_export_prefix(ndl_engine *e, int slot, void *blob, size_t bytes) {
+    NDL_REQUIRE(e && blob, "null argument");
+    TRY(check_slot(e, slot));
+    const int len = e->slot_mark[slot];
+    const size_t need = prefix_blob_bytes(e->dc.layers, e->dc.heads, len);
+    NDL_REQUIRE(bytes >= need, "primed prefix buffer too small (%zu bytes, %zu needed)", bytes, need);
+    *static_cast<int32_t *>(blob) = len;
+    if (len == 0) return NDL_OK;
+    uint8_t *stage = nullptr;
+    NDL_CUDA(cudaMallocAsync(reinterpret_cast<void **>(&stage), need, e->stream));
+    int st = launch_prefix_move(true, e->dc.layers, e->dc.heads, len, e->d_page_table + (size_t)slot * e->max_pages,
+                                e->pool, (long long)e->page_bytes, e->ec.kv_pages, stage, e->d_status, e->stream);
+    if (st == NDL_OK && cudaMemcpyAsync(static_cast<uint8_t *>(blob) + 4, stage + 4, need - 4, cudaMemcpyDeviceToHost,
+                                        e->stream) != cudaSuccess)
+        st = set_error(NDL_ERR_CUDA, "primed prefix download failed");
+    cudaFreeAsync(stage, e->stream);
+    TRY(st);
+    return check_status(e);
+}
+
+// Engine.ImportPrimedPrefix (src/Needle/Engine.cs:429-464): the slot's cache
+// becomes the blob's prefix; its length and mark are the blob's length.
+NDL_API int ndl_slot_import_prefix(ndl_engine *e, int slot, const void *blob, size_t bytes) {
+    NDL_REQUIRE(e && blob, "null argument");
+    TRY(check_slot(e, slot));
+    NDL_REQUIRE(bytes >= 4, "primed prefix is truncated");
+    const int len = *static_cast<const int32_t *>(blob);
+    NDL_REQUIRE(len >= 0 && len <= e->ec.capacity, "primed prefix length exceeds context capacity");
+    const size_t need = prefix_blob_bytes(e->dc.layers, e->dc.heads, len);
+    NDL_REQUIRE(bytes >= need, "primed prefix is truncated");
+    TRY(ndl_slot_reset(e, slot));
+    if (len > 0) {
+        TRY(reserve_pages(e, slot, 0, len));
+        uint8_t *stage = nullptr;
+        NDL_CUDA(cudaMallocAsync(reinterpret_cast<void **>(&stage), need, e->stream));
+        int st = cudaMemcpyAsync(stage, blob, need, cudaMemcpyHostToDevice, e->stream) == cudaSuccess
+                     ? launch_prefix_move(false, e->dc.layers, e->dc.heads, len,
+                                          e->d_page_table + (size_t)slot * e->max_pages, e->pool,
+                                          (long long)e->page_bytes, e->ec.kv_pages, stage, e->d_status, e->stream)
+                     : set_error(NDL_ERR_CUDA, "primed prefix upload failed");
+        cudaFreeAsync(stage, e->stream);
+        TRY(st);
+        TRY(check_status(e));
+    }
+    e->slot_len[slot] = len;
+    e->slot_mark[slot] = len;
+    return NDL_OK;
+}
+
+// Prefix sharing: `dst` takes `src`'s marked prefix by reference.  Whole
+// pages are shared (one more reference each); the partial last page is
+// copied.  A later write into a shared page copies it first (copy on write),
+// so neither slot sees the other's new positions.
+NDL_API int ndl_slot_share_prefix(ndl_engine *e, int dst, int src) {
+    NDL_REQUIRE(e, "null engine");
+    TRY(check_slot(e, dst));
+    TRY(check_slot(e, src));
+    NDL_REQUIRE(dst != src, "slot %d cannot share its own prefix", dst);
+    const int len = e->slot_mark[src];
+    TRY(ndl_slot_reset(e, dst));
+    std::vector<int32_t> updates, copies;
+    const int32_t *rs = e->page_table.data() + (size_t)src * e->max_pages;
+    int32_t *rd = e->page_table.data() + (size_t)dst * e->max_pages;
+    const int whole = len / kPagePositions;
+    for (int p = 0; p < whole; p++) {
+        rd[p] = rs[p];
+        e->page_refs[rs[p]]++;
+        updates.insert(updates.end(), {dst, p, rd[p]});
+    }
+    if (len % kPagePositions) {
+        const int page = alloc_page(e);
+        if (page < 0) {
+            push_page_updates(e, updates);
+            return set_error(NDL_ERR_PAGES_EXHAUSTED, "KV page pool exhausted");
+        }
+        copies.insert(copies.end(), {rs[whole], page});
+        rd[whole] = page;
+        updates.insert(updates.end(), {dst, whole, page});
+    }
+    TRY(copy_pages(e, copies));
+    TRY(push_page_updates(e, updates));
+    e->slot_len[dst] = len;
+    e->slot_mark[dst] = len;
+    e->cross_slot[dst] = e->cross_slot[src];
     return NDL_OK;
 }
 

@@ -90,6 +90,13 @@ struct AttnArgs {
     AttnWork *work;   // [rows * heads * max_chunks] items, compacted
     int *n_work;      // the list's length
 };
+// Primed-prefix blobs (prefix.cu): bytes of a blob of `len` positions, and
+// the move of a slot's first `len` positions between its pages and a blob
+// (to_blob) or back.
+size_t prefix_blob_bytes(int layers, int heads, int len);
+int launch_prefix_move(bool to_blob, int layers, int heads, int len, const int32_t *pages, uint8_t *pool,
+                       long long page_bytes, int num_pages, uint8_t *blob, int *status, cudaStream_t stream);
+
 // Builds the compacted work list of a launch shape (one small launch; the
 // engine builds it once per step and reuses it for every layer).
 int launch_attn_work(const AttnArgs &a, cudaStream_t stream);

@@ -166,6 +166,33 @@ class BatchedEngine:
         """Engine.CopyFrom (Engine.cs:367-379): dst becomes a copy of src."""
         call("ndl_slot_copy", self._h, dst, src)
 
+    # -- primed prefixes (Engine.cs:398-464) and prefix sharing --
+    def prefix_bytes(self, slot):
+        """Engine.PrimedPrefixBytes: bytes of the slot's marked-prefix blob."""
+        n = ctypes.c_size_t()
+        call("ndl_slot_prefix_bytes", self._h, slot, ctypes.byref(n))
+        return n.value
+
+    def export_prefix(self, slot):
+        """Engine.ExportPrimedPrefix: the slot's marked prefix as a blob (bytes)."""
+        buf = np.empty(self.prefix_bytes(slot), np.uint8)
+        call("ndl_slot_export_prefix", self._h, slot, buf.ctypes.data, buf.size)
+        return buf.tobytes()
+
+    def import_prefix(self, slot, blob):
+        """Engine.ImportPrimedPrefix: the slot's cache becomes the blob's prefix."""
+        b = np.frombuffer(blob, np.uint8)
+        call("ndl_slot_import_prefix", self._h, slot, b.ctypes.data, b.size)
+
+    def share_prefix(self, dst, src):
+        """dst takes src's marked prefix by reference (shared pages, copy on write)."""
+        call("ndl_slot_share_prefix", self._h, dst, src)
+
+    def free_pages(self):
+        n = ctypes.c_int()
+        call("ndl_engine_free_pages", self._h, ctypes.byref(n))
+        return n.value
+
     def set_mask(self, slot, mask=None):
         """Keeps a vocabulary bitmask for `slot` on the device (None clears it)."""
         if mask is None:
