@@ -654,8 +654,103 @@ def run_beam(args, rank, world, local):
     eng.close()
 
 
+def run_prefix(args, rank, world, local):
+    """Primed tool prefix (SURVEY next-row 3): new sessions start on a
+    384-token primed prefix of the cfg2 decoder (12 layers, d 512) and decode
+    their first token, 64 sessions per step, three ways: sharing the primed
+    slot's KV pages (ndl_slot_share_prefix: whole pages by reference, the
+    partial last page copied), importing the exported blob
+    (ndl_slot_import_prefix, the reference's ImportPrimedPrefix path, blob
+    from pinned host memory), and prefilling the prefix tokens.  Each is timed
+    on the host clock (the attach steps are host page-table work plus small
+    device copies) around whole steps, each ending with the first tokens'
+    ids on the host.  value = sessions per second through sharing."""
+    import torch
+
+    entry.load_package().lib()
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    eng_mod = __import__("needle_cs_b200.engine", fromlist=["engine"])
+    P, B = 384, 64
+    eng = eng_mod.BatchedEngine(eng_mod.SyntheticDecoder(seed=1), slots=1 + B, context_length=512, chunk_size=512,
+                                max_heads=B, device=local)
+    eng.fill_synthetic(0, P, 7, rank)
+    eng.mark_slot(0)
+    blob = eng.export_prefix(0)
+    pinned = torch.empty(len(blob), dtype=torch.uint8).pin_memory()
+    pinned.numpy()[:] = np.frombuffer(blob, np.uint8)
+    blob_view = pinned.numpy()
+    slots = np.arange(1, 1 + B, dtype=np.int32)
+    prompt = np.random.default_rng(rank).integers(0, 8192, P).astype(np.int32)
+    first = np.full(B, 17, np.int32)
+
+    def shared():
+        for sl in slots:
+            eng.share_prefix(int(sl), 0)
+        eng.forward_batch(first, slots, np.arange(B, dtype=np.int32))
+        return eng.sample_argmax()
+
+    def imported():
+        for sl in slots:
+            call_import(int(sl))
+        eng.forward_batch(first, slots, np.arange(B, dtype=np.int32))
+        return eng.sample_argmax()
+
+    def call_import(sl):
+        eng_mod.call("ndl_slot_import_prefix", eng._h, sl, blob_view.ctypes.data, blob_view.size)
+
+    def prefilled():
+        for sl in slots:
+            eng.reset_slot(int(sl))
+        rows_per = 512 // (P + 1)  # whole sessions per 512-row chunk
+        for lo in range(0, B, rows_per):
+            grp = slots[lo:lo + rows_per]
+            toks = np.concatenate([np.append(prompt, 17) for _ in grp]).astype(np.int32)
+            rs = np.repeat(grp, P + 1).astype(np.int32)
+            heads = np.arange(P, len(toks), P + 1, dtype=np.int32)
+            eng.forward_batch(toks, rs, heads)
+            eng.sample_argmax()
+
+    def timed(fn, reps):
+        for _ in range(max(3, args.warmup)):
+            fn()
+        eng.sync()
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            fn()
+        eng.sync()
+        return (time.perf_counter() - t0) / reps
+
+    reps = max(3, min(args.steps, 20))
+    barrier(world)
+    with ClockSampler(torch.cuda.get_device_properties(device).uuid) as clocks:
+        t_share = max_over_ranks(timed(shared, reps), world)
+        t_import = max_over_ranks(timed(imported, reps), world)
+        t_prefill = max_over_ranks(timed(prefilled, max(3, reps // 4)), world)
+    ids_a = shared()
+    ids_b = imported()
+    line = {"metric": "primed sessions/sec/box (attach + first token)", "value": world * B / t_share,
+            "unit": "sessions/s", "n_gpus": world, "steps": reps, "warmup": max(3, args.warmup),
+            "ms_per_step": t_share * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int8xint8->int32,f32", "data": "synthetic",
+            "config": {"workload": "primed_prefix", "model": "synthetic needle-3-shaped decoder (cfg2)",
+                       "prefix_tokens": P, "sessions_per_step": B, "blob_bytes": len(blob),
+                       "paths": "share = page references (+ partial page copy); import = blob upload; "
+                                "prefill = the prefix tokens through the model"},
+            "import_sessions_per_s": world * B / t_import, "prefill_sessions_per_s": world * B / t_prefill,
+            "import_blob_gbs": world * B * len(blob) / t_import / 1e9,
+            "same_first_tokens_share_vs_import": bool(np.array_equal(ids_a, ids_b)),
+            "roofline": None,
+            "e2e": {"value": world * B / t_share, "unit": "sessions/s", "h2d_bytes_per_step": B * 4 * 3,
+                    "d2h_bytes_per_step": B * 4},
+            "gpu_launches": reps * (12 * 10 + 5), "clocks": clocks.summary()}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    eng.close()
+
+
 WORKLOADS = {"cfg1": GemvWorkload, "cfg2": DecodeWorkload, "cfg3": ServingWorkload, "cfg4": BeamWorkload,
-             "cfg5": DecodeWorkload}
+             "cfg5": DecodeWorkload, "prefix": None}
 DECODE = ("cfg2", "cfg5")
 
 
@@ -896,6 +991,8 @@ def main():
             run_serving(args, rank, world, local)
         elif args.workload == "cfg4":
             run_beam(args, rank, world, local)
+        elif args.workload == "prefix":
+            run_prefix(args, rank, world, local)
         else:
             run_ours(args, rank, world, local)
     finally:
