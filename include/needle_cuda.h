@@ -330,6 +330,11 @@ NDL_API int ndl_slot_import_prefix(ndl_engine *e, int slot, const void *blob, si
  * a later write into a shared page copies it first (copy on write).  dst's
  * length and mark become the prefix length. */
 NDL_API int ndl_slot_share_prefix(ndl_engine *e, int dst, int src);
+/* Times the last step's self-attention launch of `layer` alone: `reps`
+ * back-to-back launches with the step's rows, pages and work list between two
+ * events on the engine stream; *ms_per_launch = their average.  A measurement
+ * aid (the attention roofline); it rewrites only the step's scratch outputs. */
+NDL_API int ndl_engine_time_attention(ndl_engine *e, int layer, int reps, float *ms_per_launch);
 /* Pool pages not held by any slot. */
 NDL_API int ndl_engine_free_pages(ndl_engine *e, int *free_pages);
 

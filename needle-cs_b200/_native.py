@@ -70,6 +70,7 @@ SIGNATURES = {
     "ndl_slot_import_prefix": (c_int, [c_void_p, c_int, c_void_p, c_size_t]),
     "ndl_slot_share_prefix": (c_int, [c_void_p, c_int, c_int]),
     "ndl_engine_free_pages": (c_int, [c_void_p, ctypes.POINTER(c_int)]),
+    "ndl_engine_time_attention": (c_int, [c_void_p, c_int, c_int, ctypes.POINTER(c_float)]),
     "ndl_selftest_bounded_wait": (c_int, [c_int]),
     "ndl_kt_quantize_int8": (c_float, [c_void_p, c_int, c_void_p]),
     "ndl_kt_argmax_masked": (c_int, [c_void_p, c_void_p, c_int, c_int]),

@@ -1055,6 +1055,39 @@ NDL_API int ndl_engine_get_info(ndl_engine *e, ndl_engine_info *info) {
     return NDL_OK;
 }
 
+// Times the last step's self-attention launch of `layer` alone: `reps`
+// back-to-back launches (the step's rows, KV pages and work list) between
+// two events on the engine stream; *ms = the average launch.  A measurement
+// aid for the attention roofline: the launches rewrite the step's scratch
+// outputs (the query is the last layer's), nothing a later step reads.
+NDL_API int ndl_engine_time_attention(ndl_engine *e, int layer, int reps, float *ms) {
+    NDL_REQUIRE(e && ms, "null argument");
+    NDL_REQUIRE(e->last_rows > 0, "no step has run");
+    NDL_REQUIRE(layer >= 0 && layer < e->dc.layers && reps >= 1, "layer %d / reps %d out of range", layer, reps);
+    const int rows = e->last_rows;
+    const int32_t *d_slot = e->d_meta + e->off_slot, *d_pos = e->d_meta + e->off_pos;
+    const int32_t *d_order = e->d_meta + e->off_order;
+    const int max_chunks = (e->max_pages + kAttnChunkPages - 1) / kAttnChunkPages;
+    const AttnArgs aa{e->q8, e->qs, d_slot, d_pos, d_order, e->d_page_table, e->max_pages, e->pool,
+                      (long long)e->page_bytes, e->ec.kv_pages, layer, e->dc.heads, rows, kAttnChunkPages,
+                      max_chunks, 1.0f / sqrtf((float)e->dc.head_dim), e->attn, e->partials, e->arrivals,
+                      e->d_status, e->ec.slots, e->qa, e->sa, e->attn_work, e->n_work};
+    cudaEvent_t t0 = nullptr, t1 = nullptr;
+    NDL_CUDA(cudaEventCreate(&t0));
+    NDL_CUDA(cudaEventCreate(&t1));
+    int st = cudaEventRecord(t0, e->stream) == cudaSuccess ? NDL_OK : set_error(NDL_ERR_CUDA, "event record");
+    for (int r = 0; r < reps && st == NDL_OK; r++) st = launch_attn_decode(aa, e->stream, false, false);
+    float total = 0.0f;
+    if (st == NDL_OK && (cudaEventRecord(t1, e->stream) != cudaSuccess || cudaEventSynchronize(t1) != cudaSuccess ||
+                         cudaEventElapsedTime(&total, t0, t1) != cudaSuccess))
+        st = set_error(NDL_ERR_CUDA, "attention timing events");
+    cudaEventDestroy(t0);
+    cudaEventDestroy(t1);
+    TRY(st);
+    *ms = total / reps;
+    return check_status(e);
+}
+
 // Pool pages not held by any slot.
 NDL_API int ndl_engine_free_pages(ndl_engine *e, int *free_pages) {
     NDL_REQUIRE(e && free_pages, "null argument");

@@ -188,6 +188,12 @@ class BatchedEngine:
         """dst takes src's marked prefix by reference (shared pages, copy on write)."""
         call("ndl_slot_share_prefix", self._h, dst, src)
 
+    def time_attention(self, layer=0, reps=10):
+        """Average ms of the last step's self-attention launch of `layer`, timed alone."""
+        ms = ctypes.c_float()
+        call("ndl_engine_time_attention", self._h, layer, reps, ctypes.byref(ms))
+        return ms.value
+
     def free_pages(self):
         n = ctypes.c_int()
         call("ndl_engine_free_pages", self._h, ctypes.byref(n))
