@@ -65,7 +65,8 @@ def test_matmul_i8g32_bit_exact(ops, oracle, cuda, m, n, k):
 
 @pytest.mark.parametrize("m,n,k", [(64, 2048, 512), (128, 1536, 512), (200, 512, 2048), (512, 4096, 512),
                                    (100, 96, 96), (129, 136, 160), (512, 8192, 512), (64, 8, 32),
-                                   (96, 256, 4096)])
+                                   (96, 256, 4096), (96, 384, 192), (160, 640, 320), (300, 1000, 704),
+                                   (512, 512, 512)])
 def test_matmul_tcgen05_bit_exact(ops, oracle, cuda, m, n, k):
     """m >= 64 runs the tcgen05 kind::i8 GEMM: D and y identical to the oracle
     and to the GEMV (batch invariance across the two kernels)."""
@@ -86,7 +87,7 @@ def test_matmul_tcgen05_bit_exact(ops, oracle, cuda, m, n, k):
     assert np.array_equal(y16.cpu().numpy(), y[:16].cpu().numpy())
 
 
-@pytest.mark.parametrize("m", [4, 130])
+@pytest.mark.parametrize("m", [4, 130, 512])
 def test_matmul_residual_and_ldy(ops, oracle, cuda, m):
     n, k = 96, 256
     x, w, sw = _inputs(ops, m, n, k, seed=9)
