@@ -185,9 +185,21 @@ constexpr int kAttnConsumers = 4;  // consumer warps per CTA; warp 4 is the prod
 constexpr int kAttnStages = 3;     // ring stages per consumer
 constexpr int kAttnThreads = 32 * (kAttnConsumers + 1);
 constexpr int kAttnCtasPerSm = 2;  // 2 x 4 consumers x 3 stages x 8.7 KB = 209 KB of ring per SM
-constexpr int kConsumerSmem = kAttnStages * kKvBlockBytes + 256;  // ring + PV weight digits [4][64]
-constexpr int kAttnBarOffset = kAttnConsumers * kConsumerSmem;  // full[c][s], then empty[c][s]
-constexpr int kAttnSmem = kAttnBarOffset + 2 * kAttnConsumers * kAttnStages * 8;
+// Per-stage item header, written by the producer with the first page of an
+// item: {row, head | chunk << 16, len, pages | chunks << 16} (row -1 = the
+// list ended), the query scale at byte 16 and the 64 query bytes at byte 32.
+constexpr int kAttnHdrBytes = 96;
+constexpr int kAttnHdrOffset = kAttnStages * kKvBlockBytes + 256;
+// then the producer's landing slot for the consumer's next work-list record
+constexpr int kAttnEntryOffset = kAttnHdrOffset + kAttnStages * kAttnHdrBytes;
+constexpr int kConsumerSmem = kAttnEntryOffset + (int)sizeof(AttnWork);  // ring, digits, headers, record
+static_assert(kConsumerSmem % 16 == 0 && kAttnEntryOffset % 16 == 0, "bulk copy destinations");
+constexpr int kAttnBarOffset = kAttnConsumers * kConsumerSmem;  // full[c][s], empty[c][s], record[c]
+constexpr int kAttnSmem = kAttnBarOffset + (2 * kAttnConsumers * kAttnStages + kAttnConsumers) * 8;
+// A producer lane reads the result of its item claim (an atomic) and of a
+// query-scale load only this many SM cycles after issuing them, so the
+// warp's other lanes are not held on the load's scoreboard.
+constexpr long long kAttnLatencyCycles = 1000;
 // int32 PV accumulators gain at most 64 * 255 * 128 per page; flushing to
 // fp32 every 1024 pages keeps them below 2^31.
 constexpr int kHoldPages = 1024;
@@ -279,16 +291,30 @@ __global__ void __launch_bounds__(256) attn_work_kernel(AttnArgs a) {
         const int head = t / nc, chunk = t - head * nc;
         if (attn_item(a, (ri * a.heads + head) * a.max_chunks + chunk, it)) a.work[base + t] = attn_work_of(a, it);
     }
-    if (ri == a.rows - 1 && threadIdx.x == 0) *a.n_work = base + items;
+    if (ri == a.rows - 1 && threadIdx.x == 0) {
+        a.n_work[0] = base + items;
+        a.n_work[1] = 0;  // the decode kernel's item counter and finish count
+        a.n_work[2] = 0;
+    }
 }
 
-// Persistent, warp-specialised.  Items of the work list are dealt to the
-// consumer warps of the grid in snake order (round r gives consumer w the
-// item r*W + w for even r, r*W + W-1-w for odd r; rows are sorted longest
-// first).  Lane c of the producer warp feeds consumer c of its CTA: it
-// issues that consumer's page copies (one cp.async.bulk per 8704-byte page
-// record) into the consumer's 3-stage ring as stages free up, so a consumer
-// never waits on a copy's issue; lanes with a free stage issue together.
+// Persistent, warp-specialised.  The work list (rows sorted longest first,
+// heads and chunks of a row adjacent) is dealt dynamically: consumer warp w
+// takes item w first; after that, whenever its producer lane starts
+// issuing an item it claims the next unclaimed one from a counter in global
+// memory.  Warps that stream slower (the rate differs by SM and over time)
+// so take fewer items and the launch's warps finish together; claiming one
+// item ahead keeps the claims in step with progress.
+// Lane c of the producer warp feeds consumer c of its CTA.  It runs a small
+// state machine per lane so that no lane's latency holds the warp: claim
+// (atomic; its result read kAttnLatencyCycles later), fetch the item's
+// 48-byte record into shared memory (cp.async.bulk, completion polled on
+// its own mbarrier), load the query scale (read kAttnLatencyCycles later).
+// It issues the consumer's page copies (one cp.async.bulk per 8704-byte
+// page record) into the consumer's 3-stage ring as stages free up; with an
+// item's first page it writes the item header (metadata, query scale) into
+// the stage and copies the 64 query bytes beside it, so a consumer never
+// loads metadata from global memory.
 // A consumer waits for a page, moves its K and V^T fragments and scales to
 // registers, frees the stage and computes, all products on int8 tensor cores:
 //  * QK: mma.sync m16n8k32 s8, A = K (16 positions x 32 dims), B = the
@@ -301,137 +327,147 @@ __global__ void __launch_bounds__(256) attn_work_kernel(AttnArgs a) {
 //    gives exact int32 sums of digit x v, chained across pages in the
 //    accumulator until the softmax rescale changes; the digits recombine
 //    as D0 * 2^16 + D1 * 2^8 + D2 once per item.
-// Every wait and the producer's polling are bounded.
-__global__ void __launch_bounds__(kAttnThreads, kAttnCtasPerSm) attn_decode_kernel(AttnArgs a) {
-    extern __shared__ __align__(128) uint8_t smem[];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int gid = lane >> 2, tig = lane & 3;
+// Every wait and the producer's polling are bounded.  The last CTA to finish
+// returns the counters to zero for the next launch on the same list.
+__device__ __forceinline__ void attn_producer(const AttnArgs &a, uint8_t *smem, uint64_t *full, uint64_t *empty,
+                                              uint64_t *record_bar, int lane) {
     const int W = gridDim.x * kAttnConsumers;
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem + kAttnBarOffset);  // [consumer][stage]
-    uint64_t *empty = full + kAttnConsumers * kAttnStages;
-    if (threadIdx.x == 0) {
-        for (int i = 0; i < kAttnConsumers * kAttnStages; i++) mbar_init(&full[i], 1), mbar_init(&empty[i], 1);
-        fence_mbar_init();
-    }
-    __syncthreads();
-    pdl_wait();
-    pdl_trigger();
-    const int n_work = *a.n_work;
-    auto item_of = [&](int cw, int round) { return round * W + ((round & 1) ? W - 1 - cw : cw); };
-
-    if (warp == kAttnConsumers) {
-        // ---------------- producer: lane c feeds consumer c ----------------
-        const int c = lane;
-        const int cw = blockIdx.x * kAttnConsumers + c;
-        bool done = c >= kAttnConsumers;
-        int round = 0, k = 0, n_pages = 0, head = 0;
-        int pg[kAttnMaxChunkPages];
-#pragma unroll
-        for (int j = 0; j < kAttnMaxChunkPages; j++) pg[j] = -1;
-        AttnWork nx{};
-        bool nx_ok = false;
-        auto fetch = [&](int r, AttnWork &w) -> bool {  // the item of round r, if any
-            const int i = item_of(cw, r);
-            if ((long long)r * W >= n_work || i >= n_work) return false;
-            w = a.work[i];
-            return true;
-        };
-        if (!done) nx_ok = fetch(0, nx);
-        unsigned issued = 0;
-        uint32_t idle = 0;
-        bool timed_out = false;
-        while (true) {
-            bool send = false;
-            int page = -1, stage = 0;
-            if (!done && k == n_pages) {  // next item: the prefetched one; fetch the one after it
-                if (!nx_ok) {
-                    done = true;
+    const int c = lane;
+    const int n_work = a.n_work[0];
+    int *next_item = a.n_work + 1;
+    enum { kClaimed, kFetching, kScale, kReady, kExhausted };
+    bool done = c >= kAttnConsumers, ending = false;
+    uint8_t *record = smem + c * kConsumerSmem + kAttnEntryOffset;
+    AttnWork cur{}, nx{};
+    float qs_cur = 0.0f, qs_nx = 0.0f;
+    int fs = kClaimed, claim = blockIdx.x * kAttnConsumers + c;  // the first item is this warp's own
+    long long t_issue = clock64() - kAttnLatencyCycles;
+    unsigned fetches = 0;
+    int k = 0, n_pages = 0;
+    unsigned issued = 0;
+    uint32_t idle = 0;
+    bool timed_out = false;
+    while (true) {
+        bool send = false;
+        int stage = 0;
+        if (!done) {
+            // one step of the next item's fetch
+            if (fs == kClaimed && clock64() - t_issue >= kAttnLatencyCycles) {
+                if (claim < n_work) {
+                    uint64_t *bar = &record_bar[c];
+                    fence_proxy_async_smem();
+                    mbar_arrive_expect_tx(bar, (uint32_t)sizeof(AttnWork));
+                    bulk_g2s(record, a.work + claim, (uint32_t)sizeof(AttnWork), bar);
+                    fs = kFetching;
                 } else {
-                    head = nx.head_chunk & 0xFFFF;
-                    n_pages = nx.pages_chunks & 0xFFFF;
-#pragma unroll
-                    for (int j = 0; j < kAttnMaxChunkPages; j++) pg[j] = nx.page[j];
+                    fs = kExhausted;
+                }
+            } else if (fs == kFetching && mbar_test_wait(&record_bar[c], fetches & 1)) {
+                fetches++;
+                nx = *reinterpret_cast<const AttnWork *>(record);
+                qs_nx = __ldg(a.qs + (size_t)nx.row * a.heads + (nx.head_chunk & 0xFFFF));
+                t_issue = clock64();
+                fs = kScale;
+            } else if (fs == kScale && clock64() - t_issue >= kAttnLatencyCycles) {
+                fs = kReady;
+            }
+            // the next item starts once the current one is issued
+            if (!ending && k == n_pages) {
+                if (fs == kReady) {
+                    cur = nx;
+                    qs_cur = qs_nx;
+                    n_pages = cur.pages_chunks & 0xFFFF;
                     k = 0;
-                    round++;
-                    nx_ok = fetch(round, nx);
+                    claim = W + atomicAdd(next_item, 1);
+                    t_issue = clock64();
+                    fs = kClaimed;
+                } else if (fs == kExhausted) {
+                    ending = true;
                 }
             }
-            if (!done) {
+            if (ending || k < n_pages) {
                 stage = issued % kAttnStages;
                 send = issued < (unsigned)kAttnStages ||
                        mbar_test_wait(&empty[c * kAttnStages + stage], ((issued / kAttnStages) - 1) & 1);
-                if (send) {
-                    page = pg[0];
-#pragma unroll
-                    for (int j = 0; j + 1 < kAttnMaxChunkPages; j++) pg[j] = pg[j + 1];
-                    k++;
-                }
-            }
-            if (send) {  // lanes with a free stage issue together
-                uint64_t *bar = &full[c * kAttnStages + stage];
-                if (page < 0 || page >= a.num_pages) {
-                    if (a.status) atomicOr(a.status, kStatusBadPage);
-                    mbar_arrive(bar);
-                } else {
-                    const uint8_t *src = a.pool + (size_t)page * a.page_bytes + kv_block_offset(a.layer, head, a.heads);
-                    fence_proxy_async_smem();
-                    mbar_arrive_expect_tx(bar, kKvBlockBytes);
-                    bulk_g2s(smem + c * kConsumerSmem + stage * kKvBlockBytes, src, kKvBlockBytes, bar);
-                }
-                issued++;
-            }
-            const unsigned busy = __ballot_sync(0xffffffffu, !done), moved = __ballot_sync(0xffffffffu, send);
-            if (!busy) break;
-            if (moved) {
-                idle = 0;
-            } else if (++idle > kPollLimit) {
-                timed_out = true;
-                break;
-            } else {
-                __nanosleep(64);
             }
         }
-        if (timed_out && lane == 0 && a.status) atomicOr(a.status, kStatusTimeout);
-        // drain: every copy this lane issued lands before the CTA exits (bounded)
-        for (unsigned j = issued > (unsigned)kAttnStages ? issued - kAttnStages : 0u; j < issued; j++)
-            mbar_wait_bounded(&full[c * kAttnStages + j % kAttnStages], (j / kAttnStages) & 1, kWaitLimit);
-        return;
+        if (send) {  // lanes with a free stage issue together
+            uint64_t *bar = &full[c * kAttnStages + stage];
+            uint8_t *hdr = smem + c * kConsumerSmem + kAttnHdrOffset + stage * kAttnHdrBytes;
+            if (ending) {  // end marker: no copy, the consumer reads row -1 and stops
+                *reinterpret_cast<int4 *>(hdr) = make_int4(-1, 0, 0, 0);
+                mbar_arrive(bar);
+                done = true;
+            } else {
+                const bool first = k == 0;
+                int page = -1;
+#pragma unroll
+                for (int j = 0; j < kAttnMaxChunkPages; j++)
+                    if (j == k) page = cur.page[j];
+                k++;
+                const bool page_ok = page >= 0 && page < a.num_pages;
+                if (!page_ok && a.status) atomicOr(a.status, kStatusBadPage);
+                const uint32_t tx = (page_ok ? kKvBlockBytes : 0) + (first ? kHeadDim : 0);
+                const int head = cur.head_chunk & 0xFFFF;
+                if (first) {
+                    *reinterpret_cast<int4 *>(hdr) = make_int4(cur.row, cur.head_chunk, cur.len, cur.pages_chunks);
+                    *reinterpret_cast<float *>(hdr + 16) = qs_cur;
+                }
+                if (tx == 0) {
+                    mbar_arrive(bar);
+                } else {
+                    fence_proxy_async_smem();
+                    mbar_arrive_expect_tx(bar, tx);
+                    if (page_ok)
+                        bulk_g2s(smem + c * kConsumerSmem + stage * kKvBlockBytes,
+                                 a.pool + (size_t)page * a.page_bytes + kv_block_offset(a.layer, head, a.heads),
+                                 kKvBlockBytes, bar);
+                    if (first) bulk_g2s(hdr + 32, a.q + ((size_t)cur.row * a.heads + head) * kHeadDim, kHeadDim, bar);
+                }
+            }
+            issued++;
+        }
+        const unsigned busy = __ballot_sync(0xffffffffu, !done), moved = __ballot_sync(0xffffffffu, send);
+        if (!busy) break;
+        if (moved) {
+            idle = 0;
+        } else if (++idle > kPollLimit) {
+            timed_out = true;
+            break;
+        } else {
+            __nanosleep(64);
+        }
     }
+    if (timed_out && lane == 0 && a.status) atomicOr(a.status, kStatusTimeout);
+    // drain: every copy this lane issued lands before the CTA exits (bounded)
+    if (fs == kFetching) mbar_wait_bounded(&record_bar[c], fetches & 1, kWaitLimit);
+    for (unsigned j = issued > (unsigned)kAttnStages ? issued - kAttnStages : 0u; j < issued; j++)
+        mbar_wait_bounded(&full[c * kAttnStages + j % kAttnStages], (j / kAttnStages) & 1, kWaitLimit);
+}
 
-    // ---------------- consumer warp ----------------
-    const int cw = blockIdx.x * kAttnConsumers + warp;
+__device__ __forceinline__ void attn_consumer(const AttnArgs &a, uint8_t *smem, uint64_t *full, uint64_t *empty,
+                                              int warp, int lane) {
+    const int gid = lane >> 2, tig = lane & 3;
     uint8_t *ring = smem + warp * kConsumerSmem;
     uint8_t *digits = ring + kAttnStages * kKvBlockBytes;  // [digit 0..2, unused zero row][tig][16 bytes]
+    const uint8_t *headers = ring + kAttnHdrOffset;
     uint64_t *f_bar = full + warp * kAttnStages, *e_bar = empty + warp * kAttnStages;
     reinterpret_cast<uint2 *>(digits)[lane] = make_uint2(0u, 0u);
     __syncwarp();
-    // item metadata two items ahead, the query one item ahead
-    auto meta_of = [&](int r) {
-        const int i = item_of(cw, r);
-        if ((long long)r * W >= n_work || i >= n_work) return make_int4(-1, 0, 0, 0);
-        return *reinterpret_cast<const int4 *>(a.work + i);
-    };
-    auto q_of = [&](int4 m, uint4 &qv, float &qs) {
-        if (m.x < 0) return;
-        const int head = m.y & 0xFFFF;
-        // query (K dim order): chunk tig = words for both k-steps
-        qv = __ldg(reinterpret_cast<const uint4 *>(a.q + ((size_t)m.x * a.heads + head) * kHeadDim) + tig);
-        qs = __ldg(a.qs + (size_t)m.x * a.heads + head);
-    };
-    int4 meta_a = meta_of(0), meta_b = meta_of(1);
-    uint4 q_nx = make_uint4(0u, 0u, 0u, 0u);
-    float qs_nx = 0.0f;
-    q_of(meta_a, q_nx, qs_nx);
     unsigned consumed = 0;
     bool timed_out = false;
-    for (int round = 0; !timed_out; round++) {
-        const int4 meta = meta_a;
+    while (!timed_out) {
+        // the item's first stage carries its header (or the end marker)
+        const int stage0 = consumed % kAttnStages;
+        if (!mbar_wait_bounded(&f_bar[stage0], (consumed / kAttnStages) & 1, kWaitLimit)) {
+            timed_out = true;
+            break;
+        }
+        const uint8_t *hdr = headers + stage0 * kAttnHdrBytes;
+        const int4 meta = *reinterpret_cast<const int4 *>(hdr);
         if (meta.x < 0) break;  // the list ended for this warp
-        meta_a = meta_b;
-        meta_b = meta_of(round + 2);
-        const uint4 qv = q_nx;
-        const float scale = __fmul_rn(qs_nx, a.inv_sqrt_d);
-        q_of(meta_a, q_nx, qs_nx);
+        const uint4 qv = *reinterpret_cast<const uint4 *>(hdr + 32 + tig * 16);  // K-dim chunk tig, both k-steps
+        const float scale = __fmul_rn(*reinterpret_cast<const float *>(hdr + 16), a.inv_sqrt_d);
         AttnItem it;
         it.row = meta.x;
         it.head = meta.y & 0xFFFF;
@@ -452,7 +488,7 @@ __global__ void __launch_bounds__(kAttnThreads, kAttnCtasPerSm) attn_decode_kern
         const int p0 = 16 * tig + gid, p1 = p0 + 8;
         for (int pg = 0; pg < it.n_pages; pg++) {
             const int stage = consumed % kAttnStages;
-            if (!mbar_wait_bounded(&f_bar[stage], (consumed / kAttnStages) & 1, kWaitLimit)) {
+            if (pg > 0 && !mbar_wait_bounded(&f_bar[stage], (consumed / kAttnStages) & 1, kWaitLimit)) {
                 timed_out = true;
                 break;
             }
@@ -577,6 +613,37 @@ __global__ void __launch_bounds__(kAttnThreads, kAttnCtasPerSm) attn_decode_kern
         }
     }
     if (timed_out && lane == 0 && a.status) atomicOr(a.status, kStatusTimeout);
+}
+
+__global__ void __launch_bounds__(kAttnThreads, kAttnCtasPerSm) attn_decode_kernel(AttnArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + kAttnBarOffset);  // [consumer][stage]
+    uint64_t *empty = full + kAttnConsumers * kAttnStages;
+    uint64_t *record_bar = empty + kAttnConsumers * kAttnStages;  // [consumer]
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kAttnConsumers * kAttnStages; i++) mbar_init(&full[i], 1), mbar_init(&empty[i], 1);
+        for (int i = 0; i < kAttnConsumers; i++) mbar_init(&record_bar[i], 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    pdl_wait();
+    pdl_trigger();
+    if (warp == kAttnConsumers)
+        attn_producer(a, smem, full, empty, record_bar, lane);
+    else
+        attn_consumer(a, smem, full, empty, warp, lane);
+    // every producer lane has taken its last item: the last CTA out resets
+    // the item counter and the finish count for the next launch
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        if (atomicAdd(a.n_work + 2, 1) == (int)gridDim.x - 1) {
+            a.n_work[1] = 0;
+            a.n_work[2] = 0;
+            __threadfence();
+        }
+    }
 }
 
 // Combines the chunks of every long row (Attention.MergePartials,
@@ -716,7 +783,8 @@ using namespace ndl;
 static constexpr int kAbiChunkPages = 8;
 
 // Workspace: the chunk partials [rows][heads][chunks][kPartialFloats] fp32,
-// then the work list [rows * heads * chunks] and its length.
+// then the work list [rows * heads * chunks] and 16 bytes for its length and
+// the decode kernel's two counters.
 static size_t abi_partial_bytes(int rows, int heads, int max_pages) {
     const size_t chunks = (size_t)(max_pages + kAbiChunkPages - 1) / kAbiChunkPages;
     return ((size_t)rows * heads * chunks * kPartialFloats * sizeof(float) + 15) / 16 * 16;

@@ -95,7 +95,7 @@ struct ndl_engine {
     float *partials = nullptr;
     int *arrivals = nullptr;
     ndl::AttnWork *attn_work = nullptr, *cross_work = nullptr;  // per-step attention work lists
-    int *n_work = nullptr;                                 // their lengths (self, cross)
+    int *n_work = nullptr;                                 // their lengths and counters, int[4] each (self, cross)
     int *d_status = nullptr;
     int32_t *d_ids = nullptr;
     float *d_probs = nullptr, *d_logp = nullptr;
@@ -302,7 +302,7 @@ int build_buffers(ndl_engine *e) {
         const size_t items = (size_t)R * c.heads * ((e->max_pages + kAttnChunkPages - 1) / kAttnChunkPages);
         TRY(dalloc(e, &e->attn_work, items));
         if (c.cross) TRY(dalloc(e, &e->cross_work, items));
-        TRY(dalloc(e, &e->n_work, 2));
+        TRY(dalloc(e, &e->n_work, 8));  // int[4] per list (self, cross)
     }
     NDL_CUDA(cudaMemsetAsync(e->arrivals, 0, (size_t)R * c.heads * sizeof(int), e->stream));
     TRY(dalloc(e, &e->d_status, 1));
@@ -460,7 +460,7 @@ int step_kernels(ndl_engine *e, int rows, int heads) {
             w.row_slot = e->d_meta + e->off_cslot;
             w.row_pos = e->d_meta + e->off_cpos;
             w.work = e->cross_work;
-            w.n_work = e->n_work + 1;
+            w.n_work = e->n_work + 4;
             TRY(launch_attn_work(w, s));
         }
     }
@@ -509,7 +509,7 @@ int step_kernels(ndl_engine *e, int rows, int heads) {
             AttnArgs ca{e->q8, e->qs, d_cslot, d_cpos, d_order, e->d_page_table, e->max_pages, e->pool,
                         (long long)e->page_bytes, e->ec.kv_pages, l, c.heads, rows, chunk_pages, max_chunks,
                         1.0f / sqrtf((float)c.head_dim), e->attn, e->partials, e->arrivals, e->d_status,
-                        e->ec.slots, e->qa, e->sa, e->cross_work, e->n_work + 1};
+                        e->ec.slots, e->qa, e->sa, e->cross_work, e->n_work + 4};
             TRY(launch_attn_decode(ca, s, false));
             TRY(ndl_matmul_i8g32(e->qa, e->sa, rows, L.w_co, L.s_co, d, d, e->x, d, e->x, nullptr, s));
         }

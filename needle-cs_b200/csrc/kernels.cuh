@@ -88,7 +88,7 @@ struct AttnArgs {
     int8_t *q_out;    // [rows][heads * 64]
     float *s_out;     // [rows]
     AttnWork *work;   // [rows * heads * max_chunks] items, compacted
-    int *n_work;      // the list's length
+    int *n_work;      // int[4]: the list's length, the next dynamically dealt item, finished CTAs, unused
 };
 // Primed-prefix blobs (prefix.cu): bytes of a blob of `len` positions, and
 // the move of a slot's first `len` positions between its pages and a blob
