@@ -385,6 +385,24 @@ NDL_API int ndl_sample_topk(ndl_engine *e, int k, int mask_special_023, int *ids
 NDL_API int ndl_engine_set_mask(ndl_engine *e, int slot, const uint32_t *mask, int words);
 NDL_API int ndl_sample_argmax_slots(ndl_engine *e, const int *slots, int *ids, float *probs);
 
+/* Grammar-constrained sparse head: Engine.LogitsForBatchRow
+ * (src/Needle/Engine.cs:2683-2700; BatchedEngine.LogitsForBatchRow,
+ * src/Needle/BatchEngine.cs:39-40) for n <= max_heads requests at once.
+ * Request r asks for batch row rows[r] of the last forward_batch (any row,
+ * head row or not) at the vocabulary ids ids[offsets[r] .. offsets[r+1])
+ * (offsets[0] = 0, non-decreasing; ids in any order, repeats allowed).
+ *   values: host float[offsets[n]] (nullable): the logits, equal bit for bit
+ *           to the dense head's logits of that row at those ids.
+ *   picks:  host int[n] (nullable): ArgMaxSparse
+ *           (src/Needle/NeedleSession.cs:984-995), the first listed id
+ *           holding the strict maximum, -1 for an empty list.
+ *   probs:  host float[n] (nullable, needs picks): BestProbability over the
+ *           request's values (0 for an empty list).
+ * Errors: NDL_ERR_INVALID_ARG for a row outside the last step, an id outside
+ * the vocabulary or decreasing offsets.  Synchronous. */
+NDL_API int ndl_logits_sparse(ndl_engine *e, int n, const int *rows, const int *offsets, const int *ids,
+                              float *values, int *picks, float *probs);
+
 /* Engine limits. */
 typedef struct {
     int slots, capacity, vocab, max_rows, max_heads, layers, dim, heads;

@@ -60,6 +60,7 @@ SIGNATURES = {
     "ndl_sample_topk": (c_int, [c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p]),
     "ndl_engine_set_mask": (c_int, [c_void_p, c_int, c_void_p, c_int]),
     "ndl_sample_argmax_slots": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p]),
+    "ndl_logits_sparse": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
     "ndl_engine_get_info": (c_int, [c_void_p, c_void_p]),
     "ndl_slot_set_memory": (c_int, [c_void_p, c_int, c_void_p, c_int]),
     "ndl_slot_fill_memory_synthetic": (c_int, [c_void_p, c_int, c_int, c_u64, c_u64]),

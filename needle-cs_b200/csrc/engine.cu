@@ -36,6 +36,11 @@ int launch_topk_logsoftmax(const float *x, long long ldx, int n, int k, int mask
 int launch_kv_fill(uint64_t seed, uint64_t session, int layers, int heads, int first, int count,
                    const int32_t *page_row, uint8_t *pool, long long page_bytes, cudaStream_t stream);
 int launch_half_to_float(const uint16_t *src, long long n, float *dst, cudaStream_t stream);
+int launch_sparse_head(const int8_t *w, const uint16_t *sw, int vocab, int k, const int8_t *qa, const float *sa,
+                       const int32_t *offsets, int n, const int32_t *ids, int total, float *out, int *status,
+                       cudaStream_t stream);
+int launch_sparse_argmax(const float *values, const int32_t *offsets, const int32_t *ids, int n, int32_t *picks,
+                         float *probs, cudaStream_t stream);
 
 // Stream ids of the synthetic decoder tensors under the model seed.
 enum : uint64_t {
@@ -106,6 +111,10 @@ struct ndl_engine {
     int32_t *d_mask_index = nullptr;
     std::vector<char> slot_has_mask;
     void *h_out = nullptr;  // pinned sampling results
+    // sparse head staging (grown on demand): device and pinned host copies of
+    // rows, offsets, picks, probs (max_heads each) then ids and values
+    void *d_sparse = nullptr, *h_sparse = nullptr;
+    size_t sparse_bytes = 0;
     int last_rows = 0, last_heads = 0;
     int max_chunks_cap = 0;
     // captured step graphs, keyed by (rows, heads)
@@ -638,6 +647,8 @@ NDL_API int ndl_engine_destroy(ndl_engine *e) {
     for (void *p : e->allocations) cudaFree(p);
     if (e->h_meta) cudaFreeHost(e->h_meta);
     if (e->h_out) cudaFreeHost(e->h_out);
+    if (e->d_sparse) cudaFree(e->d_sparse);
+    if (e->h_sparse) cudaFreeHost(e->h_sparse);
     if (e->own_stream && e->stream) cudaStreamDestroy(e->stream);
     delete e;
     return NDL_OK;
@@ -1215,6 +1226,77 @@ NDL_API int ndl_engine_set_mask(ndl_engine *e, int slot, const uint32_t *mask, i
     NDL_CUDA(cudaMemcpyAsync(row, mask, (size_t)words * 4, cudaMemcpyHostToDevice, e->stream));
     NDL_CUDA(cudaStreamSynchronize(e->stream));
     e->slot_has_mask[slot] = 1;
+    return NDL_OK;
+}
+
+// Grows the sparse-head staging buffers to hold `total` ids: rows, offsets,
+// picks and probs (max_heads + 1 words each), then ids and values.
+static int sparse_reserve(ndl_engine *e, size_t total) {
+    const size_t bytes = ((size_t)4 * (e->ec.max_heads + 1) + 2 * total) * 4;
+    if (bytes <= e->sparse_bytes) return NDL_OK;
+    NDL_CUDA(cudaStreamSynchronize(e->stream));
+    if (e->d_sparse) cudaFree(e->d_sparse);
+    if (e->h_sparse) cudaFreeHost(e->h_sparse);
+    e->d_sparse = e->h_sparse = nullptr;
+    e->sparse_bytes = 0;
+    NDL_CUDA(cudaMalloc(&e->d_sparse, bytes));
+    NDL_CUDA(cudaMallocHost(&e->h_sparse, bytes));
+    e->sparse_bytes = bytes;
+    return NDL_OK;
+}
+
+// Engine.LogitsForBatchRow (src/Needle/Engine.cs:2683-2700) for a batch of
+// requests, with ArgMaxSparse (src/Needle/NeedleSession.cs:984-995) on top:
+// request r wants batch row rows[r] of the last forward_batch at the
+// vocabulary ids ids[offsets[r] .. offsets[r+1]).  One gather + final-norm
+// quantize of the requested rows (the dense head's kernels), one sparse
+// row-dot launch, one argmax launch.
+NDL_API int ndl_logits_sparse(ndl_engine *e, int n, const int *rows, const int *offsets, const int *ids,
+                              float *values, int *picks, float *probs) {
+    NDL_REQUIRE(e, "engine is NULL");
+    const int Hd = e->ec.max_heads, V = e->dc.vocab, d = e->dc.dim;
+    NDL_REQUIRE(n >= 0 && n <= Hd, "%d requests outside 0..%d", n, Hd);
+    NDL_REQUIRE(!probs || picks, "probs need picks");
+    if (n == 0) return NDL_OK;
+    NDL_REQUIRE(rows && offsets, "null argument");
+    NDL_REQUIRE(e->last_rows > 0, "no step has run");
+    NDL_REQUIRE(offsets[0] == 0, "offsets[0] = %d, not 0", offsets[0]);
+    for (int r = 0; r < n; r++) {
+        NDL_REQUIRE(rows[r] >= 0 && rows[r] < e->last_rows, "request %d: row %d outside the last step's %d rows", r,
+                    rows[r], e->last_rows);
+        NDL_REQUIRE(offsets[r + 1] >= offsets[r], "offsets decrease at request %d", r);
+    }
+    const int total = offsets[n];
+    NDL_REQUIRE(total == 0 || ids, "null ids");
+    for (int t = 0; t < total; t++) NDL_REQUIRE(ids[t] >= 0 && ids[t] < V, "id %d outside the vocabulary", ids[t]);
+    TRY(sparse_reserve(e, (size_t)total));
+    cudaStream_t s = e->stream;
+    int32_t *h_rows = static_cast<int32_t *>(e->h_sparse), *d_rows = static_cast<int32_t *>(e->d_sparse);
+    const size_t o_off = Hd + 1, o_picks = 2 * o_off, o_probs = 3 * o_off, o_ids = 4 * o_off, o_vals = o_ids + total;
+    memcpy(h_rows, rows, (size_t)n * 4);
+    memcpy(h_rows + o_off, offsets, (size_t)(n + 1) * 4);
+    if (total) memcpy(h_rows + o_ids, ids, (size_t)total * 4);
+    NDL_CUDA(cudaMemcpyAsync(d_rows, h_rows, o_vals * 4, cudaMemcpyHostToDevice, s));
+    float *d_vals = reinterpret_cast<float *>(d_rows + o_vals);
+    {
+        ProfScope p(e, NDL_PROF_HEAD);
+        TRY(launch_gather_rows(e->x, d_rows, n, d, e->head_x, s));
+        TRY(launch_quantize_rows(e->head_x, e->final_norm, n, d, e->qa, e->sa, s));
+        TRY(launch_sparse_head(e->w_head, e->s_head, V, d, e->qa, e->sa, d_rows + o_off, n, d_rows + o_ids, total,
+                               d_vals, e->d_status, s));
+    }
+    if (picks) {
+        ProfScope p(e, NDL_PROF_SAMPLE);
+        TRY(launch_sparse_argmax(d_vals, d_rows + o_off, d_rows + o_ids, n, d_rows + o_picks,
+                                 probs ? reinterpret_cast<float *>(d_rows + o_probs) : nullptr, s));
+        NDL_CUDA(cudaMemcpyAsync(h_rows + o_picks, d_rows + o_picks, (size_t)2 * o_off * 4, cudaMemcpyDeviceToHost, s));
+    }
+    if (values && total)
+        NDL_CUDA(cudaMemcpyAsync(h_rows + o_vals, d_vals, (size_t)total * 4, cudaMemcpyDeviceToHost, s));
+    TRY(check_status(e));
+    if (values && total) memcpy(values, h_rows + o_vals, (size_t)total * 4);
+    if (picks) memcpy(picks, h_rows + o_picks, (size_t)n * 4);
+    if (probs) memcpy(probs, h_rows + o_probs, (size_t)n * 4);
     return NDL_OK;
 }
 

@@ -218,6 +218,29 @@ class BatchedEngine:
              probs.ctypes.data if with_probs else None)
         return (ids, probs) if with_probs else ids
 
+    def logits_sparse(self, rows, id_lists, values=True, pick=False, with_probs=False):
+        """Engine.LogitsForBatchRow for several requests: the logits of batch
+        row rows[r] of the last step at the vocabulary ids id_lists[r]; with
+        pick, ArgMaxSparse's id per request (and BestProbability with
+        with_probs).  Returns (values per request, picks, probs), absent parts
+        None."""
+        rw = _i32(rows)
+        lists = [_i32(x) for x in id_lists]
+        assert len(lists) == rw.size, (len(lists), rw.size)
+        offsets = np.zeros(rw.size + 1, np.int32)
+        offsets[1:] = np.cumsum([x.size for x in lists])
+        flat = np.concatenate(lists) if lists else np.zeros(0, np.int32)
+        flat = np.ascontiguousarray(flat, np.int32)
+        total = int(offsets[-1])
+        vals = np.empty(max(total, 1), np.float32) if values else None
+        picks = np.empty(max(rw.size, 1), np.int32) if (pick or with_probs) else None
+        probs = np.empty(max(rw.size, 1), np.float32) if with_probs else None
+        call("ndl_logits_sparse", self._h, rw.size, rw.ctypes.data, offsets.ctypes.data,
+             flat.ctypes.data if total else None, vals.ctypes.data if values else None,
+             picks.ctypes.data if picks is not None else None, probs.ctypes.data if with_probs else None)
+        per = [vals[offsets[r]:offsets[r + 1]].copy() for r in range(rw.size)] if values else None
+        return per, (picks[:rw.size] if picks is not None else None), (probs[:rw.size] if with_probs else None)
+
     def sample_topk(self, k, mask_special_023=False, with_probs=False):
         n = self._last_heads
         ids = np.empty((n, k), np.int32)

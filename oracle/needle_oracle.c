@@ -465,6 +465,21 @@ float ndo_best_probability(const float *values, int count, float best) {
     return 1.0f / total;
 }
 
+/* NeedleSession.ArgMaxSparse (src/Needle/NeedleSession.cs:984-995): over
+ * the values of a sparse head list (Engine.LogitsForBatchRow order), the id
+ * of the first entry holding the strict maximum (-1 when no value exceeds
+ * -inf) and BestProbability over all listed values (0 when none). */
+int ndo_argmax_sparse(const float *values, const int32_t *rows, int count, float *probability) {
+    int best = -1;
+    float peak = -INFINITY;
+    for (int i = 0; i < count; i++) {
+        float value = values[i];
+        if (value > peak) { peak = value; best = rows[i]; }
+    }
+    *probability = best < 0 ? 0.0f : ndo_best_probability(values, count, peak);
+    return best;
+}
+
 /* Ops.ArgMaxMaskedWithProbability scalar branch (Ops.cs:1302-1330). */
 int ndo_argmax_masked_with_probability(const float *x, const uint32_t *mask, int words, int length,
                                        float *scratch, float *probability) {

@@ -90,6 +90,8 @@ void ndo_merge_partials(const float *partials, int count, int heads, int stride,
 int ndo_argmax(const float *x, int n);                                       /* Ops.cs:1052-1090 scalar tail */
 int ndo_argmax_masked(const float *x, const uint32_t *mask, int words, int length); /* Ops.cs:1236-1265 */
 float ndo_best_probability(const float *values, int count, float best);      /* Ops.cs:1530-1535 */
+int ndo_argmax_sparse(const float *values, const int32_t *rows, int count,
+                      float *probability);                                   /* NeedleSession.cs:984-995 */
 int ndo_argmax_masked_with_probability(const float *x, const uint32_t *mask, int words, int length,
                                        float *scratch, float *probability);  /* Ops.cs:1302-1330 */
 void ndo_topk_logsoftmax(const float *x, int n, int k, int *indices, float *log_probs, float *probs,

@@ -51,6 +51,7 @@ _SIGS = {
     "ndo_argmax": (I, [P, I]),
     "ndo_argmax_masked": (I, [P, P, I, I]),
     "ndo_best_probability": (F, [P, I, F]),
+    "ndo_argmax_sparse": (I, [P, P, I, _c.POINTER(F)]),
     "ndo_argmax_masked_with_probability": (I, [P, P, I, I, P, _c.POINTER(F)]),
     "ndo_topk_logsoftmax": (None, [P, I, I, P, P, P, I]),
     "ndo_decoder_row": (I, [P, I, I, I, P, P, P, P, P, P, P]),
@@ -172,6 +173,16 @@ def argmax_masked(x, mask, length):
 def best_probability(values, best):
     values = f32(values)
     return lib().ndo_best_probability(ptr(values), values.size, best)
+
+
+def argmax_sparse(values, ids):
+    """ArgMaxSparse over a sparse head list: (picked id or -1, probability)."""
+    values = f32(values)
+    ids = np.ascontiguousarray(ids, np.int32)
+    assert values.size == ids.size
+    p = _c.c_float()
+    best = lib().ndo_argmax_sparse(ptr(values), ptr(ids), values.size, _c.byref(p))
+    return best, p.value
 
 
 def argmax_masked_with_probability(x, mask, length):

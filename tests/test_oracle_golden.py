@@ -38,6 +38,18 @@ def test_best_probability(oracle, golden):
     assert oracle.best_probability([0.7], 0.7) == 1.0
 
 
+def test_argmax_sparse(oracle, golden):
+    """ArgMaxSparse (NeedleSession.cs:984-995): list order decides ties, the
+    probability is BestProbability over the list (pinned by its golden)."""
+    fx = golden["fixtures"]
+    best, p = oracle.argmax_sparse([1, 2, 3], [40, 7, 12])
+    assert best == 12 and p == np.float32(fx["BestProbability_1_2_3"])
+    assert oracle.argmax_sparse([5, 9, 9, 1], [3, 8, 2, 9])[0] == 8  # first listed maximum, not the lowest id
+    assert oracle.argmax_sparse([], []) == (-1, 0.0)
+    assert oracle.argmax_sparse([-np.inf, -np.inf], [1, 2]) == (-1, 0.0)  # nothing above -inf
+    assert oracle.argmax_sparse([np.nan, 2.0], [4, 6])[0] == 6  # NaN never wins
+
+
 def test_rms_unit(oracle, golden):
     x = np.float32([3.0, 4.0])
     inv = oracle.lib().ndo_inverse_rms(oracle.ptr(x), 2)
