@@ -215,6 +215,92 @@ class GemvWorkload:
         return calls * self.unit_bytes / dt / 1e9, f"{calls} calls of the M={m} linear, 1 weight set (L2/LLC-warm)"
 
 
+class CqWorkload:
+    """The reference's own weight format (Needle 3 CQ): y = MatMulRows(W,
+    Prepare(x)) for M tokens on [2048, 512] matrices of 2-bit codebook indices
+    with one fp16 norm per (row, 128 columns) -- the cfg1 shape in CQ form.
+    One step = the matmul over `copies` distinct matrices stacked into one
+    launch (weights cycled so they stream from HBM)."""
+
+    name = "cq_linear"
+    metric = "CQ linear GB/s (algorithmic bytes)"
+    kernel = "cq_matmul_kernel<2> (codebook byte permutes + dp4a)"
+    dtype = "u2 codes x int8 -> int32, f32"
+
+    def __init__(self, m=16, n=2048, k=512, bits=2, copies=768):
+        self.m, self.n, self.k, self.bits, self.copies = m, n, k, bits, copies
+        stride = ((k // 128) + 7) & ~7
+        self.unit_bytes = n * k * bits // 8 + n * (k // 128) * 2 + m * k + 2 * m * stride * 4 + m * n * 4
+
+    def setup(self, device):
+        import torch
+
+        self.ops = __import__("needle_cs_b200.ops", fromlist=["ops"])
+        ops = self.ops
+        m, n, k, c, bits = self.m, self.n, self.k, self.copies, self.bits
+        gen = torch.Generator(device=device).manual_seed(11)
+        self.idx = torch.randint(0, 256, (c * n, k * bits // 8), dtype=torch.uint8, device=device, generator=gen)
+        self.norms = (torch.rand((c * n, k // 128), device=device, generator=gen) * 1.8 + 0.2).half().view(
+            torch.int16)
+        levels = np.array([-0.6, -0.2, 0.2, 0.6] if bits == 2 else [(i - 7.5) * 0.1 for i in range(16)], np.float32)
+        peak = float(np.abs(levels).max())
+        self.byte_scale = np.float32(peak / 63.0)
+        self.book = (np.rint(np.resize(levels, 16) / self.byte_scale) + 63).astype(np.uint8)
+        self.x_host = torch.from_numpy(ops.synth_normal_f32(0, 1, m * k).reshape(m, k)).pin_memory()
+        self.x = self.x_host.to(device)
+        self.v, self.sc, self.off = ops.cq_prepare(self.x, bits)
+        self.y = torch.empty((m, c * n), dtype=torch.float32, device=device)
+        self.y_host = torch.empty((m, n), dtype=torch.float32).pin_memory()
+        self.x_dev = torch.empty_like(self.x)
+        self.v1, self.sc1, self.off1 = torch.empty_like(self.v), torch.empty_like(self.sc), torch.empty_like(self.off)
+        self.y1 = torch.empty((m, n), dtype=torch.float32, device=device)
+        torch.cuda.synchronize()
+
+    def step(self):
+        self.ops.cq_matmul(self.idx, self.norms, self.book, self.byte_scale, self.bits, self.v, self.sc, self.off,
+                           y=self.y)
+        return 1
+
+    def units_per_step(self):
+        return self.copies
+
+    def bytes_per_step(self):
+        return self.copies * self.unit_bytes
+
+    def e2e_step(self):
+        """Public-API calls with host buffers: H2D of x, Prepare, MatMulRows on one matrix, D2H of y."""
+        self.x_dev.copy_(self.x_host, non_blocking=True)
+        self.ops.cq_prepare(self.x_dev, self.bits, self.v1, self.sc1, self.off1)
+        self.ops.cq_matmul(self.idx[:self.n], self.norms[:self.n], self.book, self.byte_scale, self.bits, self.v1,
+                           self.sc1, self.off1, y=self.y1)
+        self.y_host.copy_(self.y1, non_blocking=True)
+        return 2, self.x_host.numel() * 4, self.y_host.numel() * 4
+
+    def describe(self):
+        return {"workload": self.name, "m": self.m, "n": self.n, "k": self.k, "bits": self.bits,
+                "weight_copies": self.copies, "group": 128,
+                "l2": "inputs exceed L2 (weights cycled over %d MiB)" % (self.copies * self.n * self.k * self.bits // 8
+                                                                       >> 20)}
+
+    def cpu_sample(self, oracle, budget_s=10.0):
+        """The oracle's scalar MatMulRows on one matrix, same shapes."""
+        m, n, k, bits = self.m, self.n, self.k, self.bits
+        rng = np.random.default_rng(11)
+        idx = rng.integers(0, 256, (n, k * bits // 8), dtype=np.uint8)
+        norms = (rng.uniform(0.2, 2.0, (n, k // 128))).astype(np.float16).view(np.uint16)
+        levels = [-0.6, -0.2, 0.2, 0.6] if bits == 2 else [(i - 7.5) * 0.1 for i in range(16)]
+        book = oracle.codebook(np.array(levels, np.float32), len(levels))
+        vals, sc, off, _ = oracle.prepare_cq(self.ops.synth_normal_f32(0, 1, m * k).reshape(m, k), bits)
+        calls, t0 = 0, time.perf_counter()
+        while True:
+            oracle.matmul_rows_cq(idx, norms, book, bits, vals, sc, off)
+            calls += 1
+            dt = time.perf_counter() - t0
+            if dt >= budget_s or calls >= 200:
+                break
+        return calls * self.unit_bytes / dt / 1e9, f"{calls} calls of the M={m} CQ matmul, 1 matrix (L2/LLC-warm)"
+
+
 class DecodeWorkload:
     """Batched greedy decode of the synthetic 12-layer decoder.
 
@@ -750,7 +836,7 @@ def run_prefix(args, rank, world, local):
 
 
 WORKLOADS = {"cfg1": GemvWorkload, "cfg2": DecodeWorkload, "cfg3": ServingWorkload, "cfg4": BeamWorkload,
-             "cfg5": DecodeWorkload, "prefix": None}
+             "cfg5": DecodeWorkload, "prefix": None, "cq": CqWorkload}
 DECODE = ("cfg2", "cfg5")
 
 
@@ -789,10 +875,11 @@ def run_reference(args, rank, world):
             if i >= args.warmup:
                 per_step.append(v)
         value = statistics.median(per_step)
-        metric, unit = LINEAR_METRIC, "GB/s"
+        metric, unit = getattr(wl, "metric", LINEAR_METRIC), "GB/s"
     line = {"impl": "reference", "metric": metric, "value": value, "unit": unit,
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "int8xint8->int32,f32", "data": "synthetic",
+            "scaling": "weak", "vs_baseline": None, "dtype": getattr(wl, "dtype", "int8xint8->int32,f32"),
+            "data": "synthetic",
             "config": wl.describe(),
             "cpu_baseline": {"value": value, "unit": unit, "cores": cores, "kind": "port", "sample": sample},
             "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -961,13 +1048,13 @@ def run_ours(args, rank, world, local):
 
     peak, peak_kind = hbm_peak()
     achieved = wl.bytes_per_step() / (per_launch_ms * 1e-3) / 1e9
-    line = {"metric": LINEAR_METRIC, "value": value, "unit": "GB/s", "n_gpus": world,
+    line = {"metric": getattr(wl, "metric", LINEAR_METRIC), "value": value, "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "int8xint8->int32,f32", "data": "synthetic",
-            "config": wl.describe(),
+            "scaling": "weak", "vs_baseline": None, "dtype": getattr(wl, "dtype", "int8xint8->int32,f32"),
+            "data": "synthetic", "config": wl.describe(),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": None, "peak_source": peak_kind,
-                         "kernel": "gemv_i8g32_reg_kernel<2> (K 512: activations in registers)"},
+                         "kernel": getattr(wl, "kernel", "gemv_i8g32_reg_kernel<2> (K 512: activations in registers)")},
             "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_call": e_ms},
             "gpu_launches": launches,

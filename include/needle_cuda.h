@@ -206,6 +206,50 @@ NDL_API float ndl_kt_quantize_int8(const float *x, int n, int8_t *destination);
 NDL_API int ndl_kt_argmax_masked(const float *x, const uint32_t *mask, int words, int length);
 NDL_API float ndl_kt_best_probability(const float *values, int count, float best);
 
+/* CQ weights (the reference's `.cact` matrices): Codebook, Cq and
+ * Activations with the reference's sequential layouts (src/Needle/Model.cs:8-52,
+ * src/Needle/Quant.cs:11-42).
+ *   MatMulRows  void(Cq* w, Activations* a, int tokens, float* y, int ldy,
+ *               int rowStart, int rowEnd)  slot 0: y[t*ldy + n] for n in
+ *               [rowStart, rowEnd) only, equal bit for bit to Scalar.MatMulRows
+ *               (src/Needle/Scalar.cs:146-192).
+ *   Prepare     void(float* x, int tokens, int cols, int bits, Activations* a)
+ *               slot 1: Quant.PrepareRange's scalar branch
+ *               (src/Needle/Quant.cs:471-484), bit for bit. */
+typedef struct {
+    float levels[16];
+    uint8_t bytes[32];
+    float byte_scale;
+} ndl_kt_codebook;
+typedef struct {
+    const uint8_t *indices;  /* [rows][cols * bits / 8] */
+    const uint16_t *norms;   /* [rows][cols / 128] fp16 */
+    const ndl_kt_codebook *book;
+    int rows, cols, bits;
+} ndl_kt_cq;
+typedef struct {
+    int8_t *values;  /* [tokens][cols], plane order */
+    float *scales;   /* [tokens][stride] */
+    float *offsets;  /* [tokens][stride] */
+    int cols, groups, stride;
+} ndl_kt_activations;
+NDL_API void ndl_kt_matmul_rows(const ndl_kt_cq *w, const ndl_kt_activations *a, int tokens, float *y, int ldy,
+                                int row_start, int row_end);
+NDL_API void ndl_kt_prepare(const float *x, int tokens, int cols, int bits, const ndl_kt_activations *a);
+
+/* The same two operations on device memory, stream-ordered: CQ activation
+ * prep for `tokens` rows of x [tokens][cols] (values [tokens][cols], scales
+ * and offsets [tokens][stride]) and the CQ matmul y[t*ldy + n] for n in
+ * [row_start, row_end) of a [rows][cols] CQ matrix (book_bytes: the
+ * codebook's 16 level bytes, host memory).  cols a multiple of 128 up to
+ * 8192; bits 2 or 4. */
+NDL_API int ndl_cq_prepare(const float *x, int tokens, int cols, int bits, int8_t *values, float *scales,
+                           float *offsets, int stride, void *stream);
+NDL_API int ndl_cq_matmul(const uint8_t *indices, const uint16_t *norms, const uint8_t *book_bytes, float byte_scale,
+                          int rows, int cols, int bits, const int8_t *values, const float *scales,
+                          const float *offsets, int stride, int tokens, float *y, int ldy, int row_start, int row_end,
+                          void *stream);
+
 /* ------------------------------------------------------------------ */
 /* Batched decode engine (replaces BatchedEngine + EngineCore slots)   */
 /* ------------------------------------------------------------------ */

@@ -61,6 +61,9 @@ SIGNATURES = {
     "ndl_engine_set_mask": (c_int, [c_void_p, c_int, c_void_p, c_int]),
     "ndl_sample_argmax_slots": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p]),
     "ndl_logits_sparse": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
+    "ndl_cq_prepare": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_int, c_void_p]),
+    "ndl_cq_matmul": (c_int, [c_void_p, c_void_p, c_void_p, ctypes.c_float, c_int, c_int, c_int, c_void_p, c_void_p,
+                              c_void_p, c_int, c_int, c_void_p, c_int, c_int, c_int, c_void_p]),
     "ndl_engine_get_info": (c_int, [c_void_p, c_void_p]),
     "ndl_slot_set_memory": (c_int, [c_void_p, c_int, c_void_p, c_int]),
     "ndl_slot_fill_memory_synthetic": (c_int, [c_void_p, c_int, c_int, c_u64, c_u64]),
@@ -76,6 +79,8 @@ SIGNATURES = {
     "ndl_kt_quantize_int8": (c_float, [c_void_p, c_int, c_void_p]),
     "ndl_kt_argmax_masked": (c_int, [c_void_p, c_void_p, c_int, c_int]),
     "ndl_kt_best_probability": (c_float, [c_void_p, c_int, c_float]),
+    "ndl_kt_matmul_rows": (None, [c_void_p, c_void_p, c_int, c_void_p, c_int, c_int, c_int]),
+    "ndl_kt_prepare": (None, [c_void_p, c_int, c_int, c_int, c_void_p]),
     "ndl_beam_search": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_void_p,
                                 c_void_p, c_void_p]),
     "ndl_sched_create": (c_int, [c_void_p, c_void_p, c_void_p]),

@@ -18,6 +18,11 @@ int launch_argmax_masked(const float *x, long long ldx, const uint32_t *mask, in
                          const int32_t *mask_index, int length, int rows, int32_t *ids, float *probs,
                          cudaStream_t stream);
 int launch_best_probability(const float *x, int count, float best, float *out, cudaStream_t stream);
+int launch_cq_prepare(const float *x, int tokens, int cols, int bits, int8_t *values, float *scales, float *offsets,
+                      int stride, cudaStream_t stream);
+int launch_cq_matmul(const uint8_t *indices, const uint16_t *norms, const uint8_t *book_bytes, float byte_scale,
+                     int cols, int bits, const int8_t *values, const float *scales, const float *offsets, int stride,
+                     int tokens, float *y, int ldy, int row_start, int row_end, cudaStream_t stream);
 }  // namespace ndl
 
 namespace {
@@ -126,6 +131,80 @@ NDL_API float ndl_kt_best_probability(const float *values, int count, float best
         return NAN;
     }
     return p;
+}
+
+
+// void MatMulRows(Cq* w, Activations* a, int tokens, float* y, int ldy, int rowStart, int rowEnd)
+// (Quant.MatMulRows on CQ weights).  Writes y[t*ldy + n] for n in [rowStart, rowEnd) only.
+NDL_API void ndl_kt_matmul_rows(const ndl_kt_cq *w, const ndl_kt_activations *a, int tokens, float *y, int ldy,
+                                int row_start, int row_end) {
+    std::lock_guard<std::mutex> lock(g_mu);
+    if (!w || !a || !y || tokens < 0 || row_start < 0 || row_end > w->rows || row_start > row_end || !w->book ||
+        (w->bits != 2 && w->bits != 4) || w->cols % 128 != 0 || a->cols != w->cols || a->stride < w->cols / 128 ||
+        ldy < row_end) {
+        set_error(NDL_ERR_INVALID_ARG, "matmul_rows: bad arguments");
+        return;
+    }
+    if (tokens == 0 || row_start == row_end) return;
+    const int rows = row_end - row_start, cols = w->cols, groups = cols / 128;
+    const size_t row_bytes = (size_t)cols * w->bits / 8;
+    const size_t b_idx = align16((size_t)rows * row_bytes), b_nrm = align16((size_t)rows * groups * 2),
+                 b_val = align16((size_t)tokens * cols), b_sc = align16((size_t)tokens * a->stride * 4),
+                 b_y = align16((size_t)tokens * rows * 4);
+    void *buf = nullptr;
+    if (scratch(b_idx + b_nrm + b_val + 2 * b_sc + b_y, &buf) != NDL_OK) return;
+    char *p = static_cast<char *>(buf);
+    uint8_t *d_idx = reinterpret_cast<uint8_t *>(p);
+    uint16_t *d_nrm = reinterpret_cast<uint16_t *>(p + b_idx);
+    int8_t *d_val = reinterpret_cast<int8_t *>(p + b_idx + b_nrm);
+    float *d_sc = reinterpret_cast<float *>(p + b_idx + b_nrm + b_val);
+    float *d_of = reinterpret_cast<float *>(p + b_idx + b_nrm + b_val + b_sc);
+    float *d_y = reinterpret_cast<float *>(p + b_idx + b_nrm + b_val + 2 * b_sc);
+    if (cudaMemcpy(d_idx, w->indices + (size_t)row_start * row_bytes, (size_t)rows * row_bytes,
+                   cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(d_nrm, w->norms + (size_t)row_start * groups, (size_t)rows * groups * 2, cudaMemcpyHostToDevice) !=
+            cudaSuccess ||
+        cudaMemcpy(d_val, a->values, (size_t)tokens * cols, cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(d_sc, a->scales, (size_t)tokens * a->stride * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(d_of, a->offsets, (size_t)tokens * a->stride * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+        launch_cq_matmul(d_idx, d_nrm, w->book->bytes, w->book->byte_scale, cols, w->bits, d_val, d_sc, d_of,
+                         a->stride, tokens, d_y, rows, 0, rows, nullptr) != NDL_OK ||
+        cudaMemcpy2D(y + row_start, (size_t)ldy * 4, d_y, (size_t)rows * 4, (size_t)rows * 4, tokens,
+                     cudaMemcpyDeviceToHost) != cudaSuccess) {
+        cudaGetLastError();
+        set_error(NDL_ERR_CUDA, "matmul_rows failed");
+    }
+}
+
+// void Prepare(float* x, int tokens, int cols, int bits, Activations* a)  (Quant.Prepare)
+NDL_API void ndl_kt_prepare(const float *x, int tokens, int cols, int bits, const ndl_kt_activations *a) {
+    std::lock_guard<std::mutex> lock(g_mu);
+    if (!x || !a || tokens < 0 || cols % 128 != 0 || cols < 128 || (bits != 2 && bits != 4) || a->cols != cols ||
+        a->stride < cols / 128) {
+        set_error(NDL_ERR_INVALID_ARG, "prepare: bad arguments");
+        return;
+    }
+    if (tokens == 0) return;
+    const int groups = cols / 128;
+    const size_t b_x = align16((size_t)tokens * cols * 4), b_val = align16((size_t)tokens * cols),
+                 b_sc = align16((size_t)tokens * a->stride * 4);
+    void *buf = nullptr;
+    if (scratch(b_x + b_val + 2 * b_sc, &buf) != NDL_OK) return;
+    char *p = static_cast<char *>(buf);
+    float *d_x = reinterpret_cast<float *>(p);
+    int8_t *d_val = reinterpret_cast<int8_t *>(p + b_x);
+    float *d_sc = reinterpret_cast<float *>(p + b_x + b_val);
+    float *d_of = reinterpret_cast<float *>(p + b_x + b_val + b_sc);
+    if (cudaMemcpy(d_x, x, (size_t)tokens * cols * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+        launch_cq_prepare(d_x, tokens, cols, bits, d_val, d_sc, d_of, a->stride, nullptr) != NDL_OK ||
+        cudaMemcpy(a->values, d_val, (size_t)tokens * cols, cudaMemcpyDeviceToHost) != cudaSuccess ||
+        cudaMemcpy2D(a->scales, (size_t)a->stride * 4, d_sc, (size_t)a->stride * 4, (size_t)groups * 4, tokens,
+                     cudaMemcpyDeviceToHost) != cudaSuccess ||
+        cudaMemcpy2D(a->offsets, (size_t)a->stride * 4, d_of, (size_t)a->stride * 4, (size_t)groups * 4, tokens,
+                     cudaMemcpyDeviceToHost) != cudaSuccess) {
+        cudaGetLastError();
+        set_error(NDL_ERR_CUDA, "prepare failed");
+    }
 }
 
 }  // extern "C"

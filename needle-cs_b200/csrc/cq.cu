@@ -1,0 +1,400 @@
+// CQ weights, the reference's own quantized format (Needle 3 `.cact`
+// records): each weight row holds 2- or 4-bit codebook indices in groups of
+// 128 columns with one fp16 norm per (row, group); a 16-entry codebook maps
+// an index to a byte level (Codebook.Fill, src/Needle/Model.cs:36-52).
+//
+// Prepare (Quant.PrepareRange scalar branch, src/Needle/Quant.cs:471-484;
+// Scalar.Hadamard / QuantizeInt8 / Planes, src/Needle/Scalar.cs:66-111):
+// per (token, 128-group) a fast Walsh-Hadamard transform scaled by 1/sqrt(128),
+// int8 quantization with one scale per group, the plane reorder that lines
+// the activations up with the packed indices, and offset = 63 * sum(q).
+//
+// MatMulRows (Scalar.MatMulRows, src/Needle/Scalar.cs:146-192): per (token,
+// row) and ascending group g, the exact int32 dot of the codebook bytes with
+// the prepared activations, then in fp32 without contraction
+//   scaled = (norm[g] * byte_scale) * scale[t][g]
+//   acc += scaled * dot;  bias += scaled * offset[t][g];   y = acc - bias.
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace ndl {
+
+constexpr float kCqHadamardScale = 0.08838834764831845f;  // Scalar.cs:49 (Quant.cs:51)
+constexpr int kCqMaxTokens = 16;                          // tokens per matmul launch (lane t folds token t)
+constexpr int kCqWarps = 8;
+constexpr int kCqMaxCols = 8192;
+
+__device__ __forceinline__ int8_t cq_quant1(float x, float inverse) {
+    const float r = rintf(__fmul_rn(x, inverse));
+    return (int8_t)(int)fminf(fmaxf(r, -128.0f), 127.0f);
+}
+
+// Warp per (token, group); lane l holds elements l, l+32, l+64, l+96.  The
+// butterflies run in the scalar order (strides 1, 2, ..., 64; lower index
+// a + b, upper a - b), strides below 32 across lanes.
+__global__ void __launch_bounds__(256) cq_prepare_kernel(const float *__restrict__ x, int tokens, int cols, int bits,
+                                                         int8_t *__restrict__ values, float *__restrict__ scales,
+                                                         float *__restrict__ offsets, int stride) {
+    pdl_enter();
+    const int groups = cols / 128;
+    const long long gw = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (gw >= (long long)tokens * groups) return;
+    const int t = (int)(gw / groups), g = (int)(gw - (long long)t * groups);
+    const float *src = x + (size_t)t * cols + (size_t)g * 128;
+    float v[4];
+#pragma unroll
+    for (int k = 0; k < 4; k++) v[k] = src[lane + 32 * k];
+#pragma unroll
+    for (int s = 1; s < 32; s <<= 1) {
+        const bool upper = (lane & s) != 0;
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const float o = __shfl_xor_sync(0xffffffffu, v[k], s);
+            v[k] = upper ? __fsub_rn(o, v[k]) : __fadd_rn(v[k], o);
+        }
+    }
+    {  // stride 32: elements (l, l+32) and (l+64, l+96)
+        const float a0 = v[0], b0 = v[1], a1 = v[2], b1 = v[3];
+        v[0] = __fadd_rn(a0, b0);
+        v[1] = __fsub_rn(a0, b0);
+        v[2] = __fadd_rn(a1, b1);
+        v[3] = __fsub_rn(a1, b1);
+    }
+    {  // stride 64: elements (l, l+64) and (l+32, l+96)
+        const float a0 = v[0], b0 = v[2], a1 = v[1], b1 = v[3];
+        v[0] = __fadd_rn(a0, b0);
+        v[2] = __fsub_rn(a0, b0);
+        v[1] = __fadd_rn(a1, b1);
+        v[3] = __fsub_rn(a1, b1);
+    }
+    float peak = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        v[k] = __fmul_rn(v[k], kCqHadamardScale);
+        peak = fmaxf(peak, fabsf(v[k]));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) peak = fmaxf(peak, __shfl_xor_sync(0xffffffffu, peak, o));
+    const float scale = peak > 0.0f ? __fdiv_rn(peak, 127.0f) : 1.0f;
+    const float inverse = __fdiv_rn(1.0f, scale);
+    int8_t *dst = values + ((size_t)t * groups + g) * 128;
+    int sum = 0;
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        const int8_t q = cq_quant1(v[k], inverse);
+        const int e = lane + 32 * k;
+        // Planes: 2-bit [p*32 + j] = q[4j + p]; 4-bit [h*64 + p*32 + j] = q[h*64 + 2j + p]
+        const int at = bits == 2 ? (e & 3) * 32 + (e >> 2) : (e >> 6) * 64 + (e & 1) * 32 + ((e & 63) >> 1);
+        dst[at] = q;
+        sum += q;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    if (lane == 0) {
+        scales[(size_t)t * stride + g] = scale;
+        offsets[(size_t)t * stride + g] = __fmul_rn(63.0f, (float)sum);
+    }
+}
+
+struct CqBook {
+    uint32_t bytes[4];  // Codebook.Bytes[0..15], little-endian words
+    float byte_scale;
+};
+
+__device__ __forceinline__ uint32_t cq_prmt(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t d;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+    return d;
+}
+// 0xFF in every byte of w whose bit `bit` (0..7) is set: the bit moves to the
+// byte's sign position and prmt's sign-replicate mode spreads it.
+template <int kBit>
+__device__ __forceinline__ uint32_t cq_bytemask(uint32_t w) {
+    return cq_prmt(w << (7 - kBit), 0u, 0xBA98u);
+}
+// prmt selector with the low (kHigh = 0) or high nibble of w's byte k in
+// nibble k.
+template <int kHigh>
+__device__ __forceinline__ uint32_t cq_nibble_sel(uint32_t w) {
+    const uint32_t u = (kHigh ? w >> 4 : w) & 0x0F0F0F0Fu;  // nibble of byte k at bits 8k..8k+3
+    return cq_prmt(u | (u >> 4), 0u, 0x0020u);            // bytes 0 and 2 hold nibbles (0, 1) and (2, 3)
+}
+// Codebook bytes of the four 2-bit indices of plane kS (bits 2kS..2kS+1 of
+// each byte): a nibble holds planes (0, 1) or (2, 3), so one selector serves
+// two planes, the low one through an index masked to 2 bits, the high one
+// shifted down.
+template <int kS>
+__device__ __forceinline__ uint32_t cq_lut2_sel(uint32_t sel, uint32_t t0) {
+    return (kS & 1) ? cq_prmt(t0, 0u, (sel >> 2) & 0x3333u) : cq_prmt(t0, 0u, sel & 0x3333u);
+}
+
+// Codebook bytes for the four 4-bit indices in the low (kS = 0) or high
+// (kS = 1) nibbles of w's bytes: the nibbles gathered into a prmt selector,
+// two 8-entry permutes and a select on the index's top bit.
+template <int kS>
+__device__ __forceinline__ uint32_t cq_lut4(uint32_t w, const uint32_t (&t)[4]) {
+    const uint32_t sel = cq_nibble_sel<kS>(w) & 0x7777u;  // index k in nibble k, top bit cleared
+    const uint32_t lo = cq_prmt(t[0], t[1], sel), hi = cq_prmt(t[2], t[3], sel);
+    const uint32_t m = cq_bytemask<kS ? 7 : 3>(w);  // bytes whose index is >= 8
+    return (hi & m) | (lo & ~m);
+}
+
+__device__ __forceinline__ uint32_t cq_lut_plane4(uint32_t w, int s, const uint32_t (&t)[4]) {
+    return s == 0 ? cq_lut4<0>(w, t) : cq_lut4<1>(w, t);
+}
+
+__device__ __forceinline__ void cq_mma(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};\n"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// Warp per tile of 16 weight rows (grid-stride), up to 16 tokens as two
+// 8-token MMA columns.  Per 128-column group and 32-column chunk k of it, the
+// codebook bytes of the chunk's indices become the A fragment of one
+// mma.sync m16n8k32 s8 (byte permutes in registers), the prepared
+// activations the B fragment (shared memory, rows padded by 16 bytes so the
+// fragment loads hit 32 distinct banks); the four chunks chain in the
+// accumulator to the exact group dot.  Chunk k of a group is plane k
+// (2-bit: bits 2k..2k+1 of bytes 0..31) or nibble k&1 of bytes 32(k>>1)..+31
+// (4-bit), matching the plane order Prepare writes.  Each lane then folds
+// its four (row, token) dots per column block into fp32 in ascending group
+// order.
+template <int kBits>
+__global__ void __launch_bounds__(32 * kCqWarps, 2) cq_matmul_kernel(
+    const uint32_t *__restrict__ indices, const uint16_t *__restrict__ norms, CqBook book, int cols,
+    const int8_t *__restrict__ values, const float *__restrict__ scales, const float *__restrict__ offsets,
+    int stride, int tokens, float *__restrict__ y, int ldy, int row_start, int row_end) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    const int groups = cols / 128, row_words = cols * kBits / 32, xstride = cols + 16;
+    constexpr int kGroupWords = kBits == 2 ? 8 : 16;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
+    uint8_t *xs = smem;                                                              // [16][cols + 16]
+    float *ss = reinterpret_cast<float *>(smem + (size_t)kCqMaxTokens * xstride);    // [16][groups]
+    float *os = ss + kCqMaxTokens * groups;
+    pdl_enter();
+    for (int i = threadIdx.x; i < kCqMaxTokens * (cols / 16); i += blockDim.x) {
+        const int t = i / (cols / 16), c = i - t * (cols / 16);
+        const uint4 v = t < tokens ? reinterpret_cast<const uint4 *>(values + (size_t)t * cols)[c]
+                                   : make_uint4(0u, 0u, 0u, 0u);
+        *reinterpret_cast<uint4 *>(xs + (size_t)t * xstride + 16 * c) = v;
+    }
+    for (int i = threadIdx.x; i < kCqMaxTokens * groups; i += blockDim.x) {
+        const int t = i / groups, g = i - t * groups;
+        ss[i] = t < tokens ? scales[(size_t)t * stride + g] : 0.0f;
+        os[i] = t < tokens ? offsets[(size_t)t * stride + g] : 0.0f;
+    }
+    __syncthreads();
+    const int n_tiles = (row_end - row_start + 15) / 16;
+    const int warps = gridDim.x * kCqWarps;
+    // two tiles per warp pass, their index words loaded a chunk of groups at a
+    // time before any is used, so each warp keeps 2 x kChunk group tiles of
+    // loads in flight
+    constexpr int kTiles = 2, kChunk = kBits == 2 ? 4 : 2, kBlocks = kBits == 2 ? 1 : 2;
+    for (int pair = blockIdx.x * kCqWarps + warp; pair * kTiles < n_tiles; pair += warps) {
+        int r0[kTiles], r1[kTiles];
+        bool ok0[kTiles], ok1[kTiles];
+        const uint32_t *w0[kTiles], *w1[kTiles];
+#pragma unroll
+        for (int tt = 0; tt < kTiles; tt++) {
+            r0[tt] = row_start + (pair * kTiles + tt) * 16 + gid;
+            r1[tt] = r0[tt] + 8;
+            ok0[tt] = r0[tt] < row_end;
+            ok1[tt] = r1[tt] < row_end;
+            w0[tt] = indices + (size_t)(ok0[tt] ? r0[tt] : row_start) * row_words;
+            w1[tt] = indices + (size_t)(ok1[tt] ? r1[tt] : row_start) * row_words;
+        }
+        float acc[kTiles][2][4], bias[kTiles][2][4];
+#pragma unroll
+        for (int tt = 0; tt < kTiles; tt++)
+#pragma unroll
+            for (int nt = 0; nt < 2; nt++)
+#pragma unroll
+                for (int i = 0; i < 4; i++) acc[tt][nt][i] = 0.0f, bias[tt][nt][i] = 0.0f;
+        for (int g0 = 0; g0 < groups; g0 += kChunk) {
+            // this lane's index words: rows r0, r1; word tig and 4 + tig of each 32-byte block
+            uint32_t c0[kTiles][kChunk][kBlocks][2], c1[kTiles][kChunk][kBlocks][2];
+            uint16_t n0[kTiles][kChunk], n1[kTiles][kChunk];
+#pragma unroll
+            for (int tt = 0; tt < kTiles; tt++)
+#pragma unroll
+                for (int cg = 0; cg < kChunk; cg++) {
+                    const int g = g0 + cg;
+                    const bool in = g < groups;
+#pragma unroll
+                    for (int h = 0; h < kBlocks; h++) {
+                        const int wi = g * kGroupWords + 8 * h + tig;
+                        c0[tt][cg][h][0] = in && ok0[tt] ? __ldg(w0[tt] + wi) : 0u;
+                        c0[tt][cg][h][1] = in && ok0[tt] ? __ldg(w0[tt] + wi + 4) : 0u;
+                        c1[tt][cg][h][0] = in && ok1[tt] ? __ldg(w1[tt] + wi) : 0u;
+                        c1[tt][cg][h][1] = in && ok1[tt] ? __ldg(w1[tt] + wi + 4) : 0u;
+                    }
+                    n0[tt][cg] = in && ok0[tt] ? norms[(size_t)r0[tt] * groups + g] : (uint16_t)0;
+                    n1[tt][cg] = in && ok1[tt] ? norms[(size_t)r1[tt] * groups + g] : (uint16_t)0;
+                }
+#pragma unroll
+            for (int cg = 0; cg < kChunk; cg++) {
+                const int g = g0 + cg;
+                if (g >= groups) break;
+#pragma unroll
+                for (int tt = 0; tt < kTiles; tt++) {
+                    const float nf0 = __fmul_rn(half_to_float_ref(n0[tt][cg]), book.byte_scale);
+                    const float nf1 = __fmul_rn(half_to_float_ref(n1[tt][cg]), book.byte_scale);
+                    int d[2][4];
+#pragma unroll
+                    for (int nt = 0; nt < 2; nt++)
+#pragma unroll
+                        for (int i = 0; i < 4; i++) d[nt][i] = 0;
+                    // 2-bit: nibble selectors of the four index words (a0..a3 order), planes (0, 1) and (2, 3)
+                    uint32_t sel_lo[4], sel_hi[4];
+                    if (kBits == 2) {
+                        const uint32_t wds[4] = {c0[tt][cg][0][0], c1[tt][cg][0][0], c0[tt][cg][0][1], c1[tt][cg][0][1]};
+#pragma unroll
+                        for (int j = 0; j < 4; j++) sel_lo[j] = cq_nibble_sel<0>(wds[j]), sel_hi[j] = cq_nibble_sel<1>(wds[j]);
+                    }
+#pragma unroll
+                    for (int k = 0; k < 4; k++) {
+                        const int h = kBits == 2 ? 0 : k >> 1;
+                        uint32_t a[4];
+                        if (kBits == 2) {
+                            const uint32_t *sel = k < 2 ? sel_lo : sel_hi;
+                            a[0] = (k & 1) ? cq_lut2_sel<1>(sel[0], book.bytes[0]) : cq_lut2_sel<0>(sel[0], book.bytes[0]);
+                            a[1] = (k & 1) ? cq_lut2_sel<1>(sel[1], book.bytes[0]) : cq_lut2_sel<0>(sel[1], book.bytes[0]);
+                            a[2] = (k & 1) ? cq_lut2_sel<1>(sel[2], book.bytes[0]) : cq_lut2_sel<0>(sel[2], book.bytes[0]);
+                            a[3] = (k & 1) ? cq_lut2_sel<1>(sel[3], book.bytes[0]) : cq_lut2_sel<0>(sel[3], book.bytes[0]);
+                        } else {
+                            a[0] = cq_lut_plane4(c0[tt][cg][h][0], k & 1, book.bytes);
+                            a[1] = cq_lut_plane4(c1[tt][cg][h][0], k & 1, book.bytes);
+                            a[2] = cq_lut_plane4(c0[tt][cg][h][1], k & 1, book.bytes);
+                            a[3] = cq_lut_plane4(c1[tt][cg][h][1], k & 1, book.bytes);
+                        }
+#pragma unroll
+                        for (int nt = 0; nt < 2; nt++) {
+                            if (nt == 1 && tokens <= 8) break;  // one 8-token column block suffices
+                            const uint8_t *xb = xs + (size_t)(nt * 8 + gid) * xstride + g * 128 + 32 * k + 4 * tig;
+                            cq_mma(d[nt], a, *reinterpret_cast<const uint32_t *>(xb),
+                                   *reinterpret_cast<const uint32_t *>(xb + 16));
+                        }
+                    }
+#pragma unroll
+                    for (int nt = 0; nt < 2; nt++)
+#pragma unroll
+                        for (int i = 0; i < 4; i++) {
+                            if (nt == 1 && tokens <= 8) break;
+                            const int t = nt * 8 + 2 * tig + (i & 1);
+                            const float scaled = __fmul_rn(i < 2 ? nf0 : nf1, ss[t * groups + g]);
+                            acc[tt][nt][i] = __fadd_rn(acc[tt][nt][i], __fmul_rn(scaled, (float)d[nt][i]));
+                            bias[tt][nt][i] = __fadd_rn(bias[tt][nt][i], __fmul_rn(scaled, os[t * groups + g]));
+                        }
+                }
+            }
+        }
+#pragma unroll
+        for (int tt = 0; tt < kTiles; tt++)
+#pragma unroll
+            for (int nt = 0; nt < 2; nt++)
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    const int t = nt * 8 + 2 * tig + (i & 1);
+                    const bool ok = i < 2 ? ok0[tt] : ok1[tt];
+                    if (ok && t < tokens)
+                        y[(size_t)t * ldy + (i < 2 ? r0[tt] : r1[tt])] = __fsub_rn(acc[tt][nt][i], bias[tt][nt][i]);
+                }
+    }
+}
+
+int launch_cq_prepare(const float *x, int tokens, int cols, int bits, int8_t *values, float *scales, float *offsets,
+                      int stride, cudaStream_t stream) {
+    if (tokens == 0) return NDL_OK;
+    const long long warps = (long long)tokens * (cols / 128);
+    launch_kernel(cq_prepare_kernel, dim3((unsigned)((warps + 7) / 8)), dim3(256), 0, stream, x, tokens, cols, bits,
+                  values, scales, offsets, stride);
+    return check_launch("cq_prepare");
+}
+
+size_t cq_matmul_smem(int cols) {
+    return (size_t)kCqMaxTokens * (cols + 16) + (size_t)2 * kCqMaxTokens * (cols / 128) * 4;
+}
+
+int launch_cq_matmul(const uint8_t *indices, const uint16_t *norms, const uint8_t *book_bytes, float byte_scale,
+                     int cols, int bits, const int8_t *values, const float *scales, const float *offsets, int stride,
+                     int tokens, float *y, int ldy, int row_start, int row_end, cudaStream_t stream) {
+    if (tokens == 0 || row_end <= row_start) return NDL_OK;
+    static int sms = 0;
+    static bool configured = false;
+    if (!configured) {
+        const int max_smem = (int)cq_matmul_smem(kCqMaxCols);
+        cudaError_t e = cudaFuncSetAttribute(cq_matmul_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(cq_matmul_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+        if (e != cudaSuccess) return set_error(NDL_ERR_CUDA, "cq matmul smem attribute: %s", cudaGetErrorString(e));
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        configured = true;
+    }
+    CqBook book;
+    memcpy(book.bytes, book_bytes, 16);
+    book.byte_scale = byte_scale;
+    const int rows = row_end - row_start;
+    for (int t0 = 0; t0 < tokens; t0 += kCqMaxTokens) {  // token chunks; each launch reads the rows once
+        const int tk = tokens - t0 < kCqMaxTokens ? tokens - t0 : kCqMaxTokens;
+        const size_t smem = cq_matmul_smem(cols);
+        long long blocks = ((rows + 31) / 32 + kCqWarps - 1) / kCqWarps;  // two 16-row tiles per warp
+        int per_sm = 1;  // resident CTAs per SM at this shared-memory size
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, bits == 2 ? cq_matmul_kernel<2> : cq_matmul_kernel<4>,
+                                                      32 * kCqWarps, smem);
+        const long long cap = (long long)sms * (per_sm > 0 ? per_sm : 1);
+        if (blocks > cap) blocks = cap;
+        const int8_t *v = values + (size_t)t0 * cols;
+        const float *sc = scales + (size_t)t0 * stride, *of = offsets + (size_t)t0 * stride;
+        float *yt = y + (size_t)t0 * ldy;
+        if (bits == 2)
+            launch_kernel(cq_matmul_kernel<2>, dim3((unsigned)blocks), dim3(32 * kCqWarps), smem, stream,
+                          reinterpret_cast<const uint32_t *>(indices), norms, book, cols, v, sc, of, stride, tk, yt,
+                          ldy, row_start, row_end);
+        else
+            launch_kernel(cq_matmul_kernel<4>, dim3((unsigned)blocks), dim3(32 * kCqWarps), smem, stream,
+                          reinterpret_cast<const uint32_t *>(indices), norms, book, cols, v, sc, of, stride, tk, yt,
+                          ldy, row_start, row_end);
+        const int st = check_launch("cq_matmul");
+        if (st != NDL_OK) return st;
+    }
+    return NDL_OK;
+}
+
+}  // namespace ndl
+
+using namespace ndl;
+
+extern "C" NDL_API int ndl_cq_prepare(const float *x, int tokens, int cols, int bits, int8_t *values, float *scales,
+                                      float *offsets, int stride, void *stream) {
+    NDL_REQUIRE(tokens >= 0 && cols >= 128 && cols % 128 == 0 && cols <= kCqMaxCols, "cols %d (a multiple of 128 up to %d)",
+                cols, kCqMaxCols);
+    NDL_REQUIRE(bits == 2 || bits == 4, "bits %d (2 or 4)", bits);
+    NDL_REQUIRE(stride >= cols / 128, "stride %d below %d groups", stride, cols / 128);
+    if (tokens == 0) return NDL_OK;
+    NDL_REQUIRE(x && values && scales && offsets, "null pointer");
+    return launch_cq_prepare(x, tokens, cols, bits, values, scales, offsets, stride, (cudaStream_t)stream);
+}
+
+extern "C" NDL_API int ndl_cq_matmul(const uint8_t *indices, const uint16_t *norms, const uint8_t *book_bytes,
+                                     float byte_scale, int rows, int cols, int bits, const int8_t *values,
+                                     const float *scales, const float *offsets, int stride, int tokens, float *y,
+                                     int ldy, int row_start, int row_end, void *stream) {
+    NDL_REQUIRE(cols >= 128 && cols % 128 == 0 && cols <= kCqMaxCols, "cols %d (a multiple of 128 up to %d)", cols,
+                kCqMaxCols);
+    NDL_REQUIRE(bits == 2 || bits == 4, "bits %d (2 or 4)", bits);
+    NDL_REQUIRE(0 <= row_start && row_start <= row_end && row_end <= rows, "rows [%d, %d) outside 0..%d", row_start,
+                row_end, rows);
+    NDL_REQUIRE(tokens >= 0 && stride >= cols / 128 && ldy >= row_end, "tokens %d / stride %d / ldy %d", tokens,
+                stride, ldy);
+    if (tokens == 0 || row_start == row_end) return NDL_OK;
+    NDL_REQUIRE(indices && norms && book_bytes && values && scales && offsets && y, "null pointer");
+    NDL_REQUIRE(aligned(indices, 4) && aligned(values, 16), "indices need 4-byte, values 16-byte alignment");
+    return launch_cq_matmul(indices, norms, book_bytes, byte_scale, cols, bits, values, scales, offsets, stride, tokens,
+                            y, ldy, row_start, row_end, (cudaStream_t)stream);
+}

@@ -116,6 +116,38 @@ def matmul_i8g32_batched(q, sa, w, sw, y):
     return y
 
 
+def cq_prepare(x, bits, values=None, scales=None, offsets=None):
+    """Quant.Prepare for CQ weights: per (token, 128 columns) FWHT, int8
+    quantize and plane reorder.  x fp32 [tokens, cols] -> (values int8
+    [tokens, cols], scales and offsets fp32 [tokens, stride])."""
+    tokens, cols = x.shape
+    stride = ((cols // 128) + 7) & ~7
+    values = torch.empty((tokens, cols), dtype=torch.int8, device=x.device) if values is None else values
+    scales = torch.empty((tokens, stride), dtype=torch.float32, device=x.device) if scales is None else scales
+    offsets = torch.empty((tokens, stride), dtype=torch.float32, device=x.device) if offsets is None else offsets
+    call("ndl_cq_prepare", _dev(x, torch.float32, "x"), tokens, cols, bits, _dev(values, torch.int8, "values"),
+         _dev(scales, torch.float32, "scales"), _dev(offsets, torch.float32, "offsets"), scales.stride(0),
+         _stream())
+    return values, scales, offsets
+
+
+def cq_matmul(indices, norms, book_bytes, byte_scale, bits, values, scales, offsets, y=None):
+    """MatMulRows on a CQ matrix: indices uint8 [rows, cols*bits/8], norms fp16
+    bits as int16 [rows, cols/128], book_bytes the codebook's 16 level bytes
+    (host); activations from cq_prepare -> y fp32 [tokens, rows]."""
+    import ctypes
+
+    rows = indices.shape[0]
+    tokens, cols = values.shape
+    y = torch.empty((tokens, rows), dtype=torch.float32, device=values.device) if y is None else y
+    table = (ctypes.c_uint8 * 16).from_buffer_copy(bytes(book_bytes[:16]))
+    call("ndl_cq_matmul", _dev(indices, torch.uint8, "indices"), _dev(norms, torch.int16, "norms"),
+         ctypes.addressof(table), float(byte_scale), rows, cols, bits, _dev(values, torch.int8, "values"),
+         _dev(scales, torch.float32, "scales"), _dev(offsets, torch.float32, "offsets"), scales.stride(0), tokens,
+         _dev(y, torch.float32, "y"), y.stride(0), 0, rows, _stream())
+    return y
+
+
 def attention_paged_workspace(rows, heads, max_pages):
     return lib().ndl_attention_paged_workspace(rows, heads, max_pages)
 

@@ -149,6 +149,47 @@ def matmul_i8g32(q, sa, w, sw, want_acc=False):
     return (y, acc) if want_acc else y
 
 
+class Codebook(_c.Structure):
+    """Codebook (src/Needle/Model.cs:36-52): levels, level bytes, byte scale."""
+    _fields_ = [("levels", _c.c_float * 16), ("bytes", _c.c_uint8 * 32), ("byte_scale", _c.c_float)]
+
+
+def codebook(levels, count):
+    """Codebook.Fill over the first `count` levels."""
+    book = Codebook()
+    lv = f32(np.resize(np.asarray(levels, np.float32), 16))
+    lib().ndo_codebook_fill(_c.byref(book), ptr(lv), count)
+    return book
+
+
+def prepare_cq(x, bits):
+    """Quant.PrepareRange scalar branch: (values [tokens][cols], scales and
+    offsets [tokens][stride], stride) for x [tokens][cols]."""
+    x = f32(x)
+    tokens, cols = x.shape
+    groups = cols // 128
+    stride = (groups + 7) & ~7
+    vals = np.zeros((tokens, cols), np.int8)
+    sc = np.zeros((tokens, stride), np.float32)
+    off = np.zeros((tokens, stride), np.float32)
+    lib().ndo_prepare_cq(ptr(x), tokens, cols, bits, ptr(vals), ptr(sc), ptr(off), stride)
+    return vals, sc, off, stride
+
+
+def matmul_rows_cq(indices, norms, book, bits, vals, sc, off, row_start=0, row_end=None, y=None):
+    """Scalar.MatMulRows on CQ weights: y [tokens][rows], rows outside
+    [row_start, row_end) left as given."""
+    indices = np.ascontiguousarray(indices, np.uint8)
+    norms = np.ascontiguousarray(norms, np.uint16)
+    tokens, cols = vals.shape
+    rows = norms.size // (cols // 128)
+    row_end = rows if row_end is None else row_end
+    y = np.zeros((tokens, rows), np.float32) if y is None else y
+    lib().ndo_matmul_rows_cq(ptr(indices), ptr(norms), _c.byref(book), rows, cols, bits, ptr(vals), ptr(sc),
+                             ptr(off), sc.shape[1], tokens, ptr(y), y.shape[1], row_start, row_end)
+    return y
+
+
 def rms_norm(x, w):
     x = f32(x)
     w = f32(w)
