@@ -236,6 +236,10 @@ typedef struct {
 NDL_API void ndl_kt_matmul_rows(const ndl_kt_cq *w, const ndl_kt_activations *a, int tokens, float *y, int ldy,
                                 int row_start, int row_end);
 NDL_API void ndl_kt_prepare(const float *x, int tokens, int cols, int bits, const ndl_kt_activations *a);
+/* GatherRow  void(Cq* w, int row, float* destination)  slot 2: Quant.GatherRow
+ * (src/Needle/Quant.cs:566-576), row decoded (Scalar.DecodeRow) and rotated
+ * per 128-column group (Scalar.Hadamard), bit for bit. */
+NDL_API void ndl_kt_gather_row(const ndl_kt_cq *w, int row, float *destination);
 
 /* The same two operations on device memory, stream-ordered: CQ activation
  * prep for `tokens` rows of x [tokens][cols] (values [tokens][cols], scales
@@ -249,6 +253,12 @@ NDL_API int ndl_cq_matmul(const uint8_t *indices, const uint16_t *norms, const u
                           int rows, int cols, int bits, const int8_t *values, const float *scales,
                           const float *offsets, int stride, int tokens, float *y, int ldy, int row_start, int row_end,
                           void *stream);
+/* GatherRow for a batch on device memory (embedding lookups): out[r] =
+ * row row_ids[r] of the CQ matrix (row_ids and out on the device, levels: the
+ * codebook's 16 float levels, host memory).  An id outside [0, rows) gives a
+ * row of zeros: ids are device data, so check them where they are made. */
+NDL_API int ndl_cq_gather_rows(const uint8_t *indices, const uint16_t *norms, const float *levels, int rows, int cols,
+                               int bits, const int32_t *row_ids, int n, float *out, void *stream);
 
 /* ------------------------------------------------------------------ */
 /* Batched decode engine (replaces BatchedEngine + EngineCore slots)   */

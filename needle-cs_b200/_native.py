@@ -62,6 +62,7 @@ SIGNATURES = {
     "ndl_sample_argmax_slots": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p]),
     "ndl_logits_sparse": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
     "ndl_cq_prepare": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_int, c_void_p]),
+    "ndl_cq_gather_rows": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_int, c_void_p, c_void_p]),
     "ndl_cq_matmul": (c_int, [c_void_p, c_void_p, c_void_p, ctypes.c_float, c_int, c_int, c_int, c_void_p, c_void_p,
                               c_void_p, c_int, c_int, c_void_p, c_int, c_int, c_int, c_void_p]),
     "ndl_engine_get_info": (c_int, [c_void_p, c_void_p]),
@@ -81,6 +82,7 @@ SIGNATURES = {
     "ndl_kt_best_probability": (c_float, [c_void_p, c_int, c_float]),
     "ndl_kt_matmul_rows": (None, [c_void_p, c_void_p, c_int, c_void_p, c_int, c_int, c_int]),
     "ndl_kt_prepare": (None, [c_void_p, c_int, c_int, c_int, c_void_p]),
+    "ndl_kt_gather_row": (None, [c_void_p, c_int, c_void_p]),
     "ndl_beam_search": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_void_p,
                                 c_void_p, c_void_p]),
     "ndl_sched_create": (c_int, [c_void_p, c_void_p, c_void_p]),

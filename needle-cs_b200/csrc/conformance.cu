@@ -23,6 +23,8 @@ int launch_cq_prepare(const float *x, int tokens, int cols, int bits, int8_t *va
 int launch_cq_matmul(const uint8_t *indices, const uint16_t *norms, const uint8_t *book_bytes, float byte_scale,
                      int cols, int bits, const int8_t *values, const float *scales, const float *offsets, int stride,
                      int tokens, float *y, int ldy, int row_start, int row_end, cudaStream_t stream);
+int launch_cq_gather(const uint8_t *indices, const uint16_t *norms, const float *levels16, int rows, int cols, int bits,
+                     const int32_t *row_ids, int n, float *out, int *status, cudaStream_t stream);
 }  // namespace ndl
 
 namespace {
@@ -204,6 +206,36 @@ NDL_API void ndl_kt_prepare(const float *x, int tokens, int cols, int bits, cons
                      cudaMemcpyDeviceToHost) != cudaSuccess) {
         cudaGetLastError();
         set_error(NDL_ERR_CUDA, "prepare failed");
+    }
+}
+
+
+// void GatherRow(Cq* w, int row, float* destination)  (Quant.GatherRow)
+NDL_API void ndl_kt_gather_row(const ndl_kt_cq *w, int row, float *destination) {
+    std::lock_guard<std::mutex> lock(g_mu);
+    if (!w || !destination || !w->book || row < 0 || row >= w->rows || (w->bits != 2 && w->bits != 4) ||
+        w->cols % 128 != 0 || w->cols < 128) {
+        set_error(NDL_ERR_INVALID_ARG, "gather_row: bad arguments");
+        return;
+    }
+    const int cols = w->cols, groups = cols / 128;
+    const size_t row_bytes = (size_t)cols * w->bits / 8;
+    const size_t b_idx = align16(row_bytes), b_nrm = align16((size_t)groups * 2), b_out = align16((size_t)cols * 4);
+    void *buf = nullptr;
+    if (scratch(b_idx + b_nrm + b_out + 16, &buf) != NDL_OK) return;
+    char *p = static_cast<char *>(buf);
+    uint8_t *d_idx = reinterpret_cast<uint8_t *>(p);
+    uint16_t *d_nrm = reinterpret_cast<uint16_t *>(p + b_idx);
+    float *d_out = reinterpret_cast<float *>(p + b_idx + b_nrm);
+    int32_t *d_row = reinterpret_cast<int32_t *>(p + b_idx + b_nrm + b_out);
+    const int32_t zero = 0;  // the one uploaded row is row 0 of the slice
+    if (cudaMemcpy(d_idx, w->indices + (size_t)row * row_bytes, row_bytes, cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(d_nrm, w->norms + (size_t)row * groups, (size_t)groups * 2, cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(d_row, &zero, 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+        launch_cq_gather(d_idx, d_nrm, w->book->levels, 1, cols, w->bits, d_row, 1, d_out, nullptr, nullptr) != NDL_OK ||
+        cudaMemcpy(destination, d_out, (size_t)cols * 4, cudaMemcpyDeviceToHost) != cudaSuccess) {
+        cudaGetLastError();
+        set_error(NDL_ERR_CUDA, "gather_row failed");
     }
 }
 

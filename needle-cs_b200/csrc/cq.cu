@@ -29,22 +29,11 @@ __device__ __forceinline__ int8_t cq_quant1(float x, float inverse) {
     return (int8_t)(int)fminf(fmaxf(r, -128.0f), 127.0f);
 }
 
-// Warp per (token, group); lane l holds elements l, l+32, l+64, l+96.  The
-// butterflies run in the scalar order (strides 1, 2, ..., 64; lower index
-// a + b, upper a - b), strides below 32 across lanes.
-__global__ void __launch_bounds__(256) cq_prepare_kernel(const float *__restrict__ x, int tokens, int cols, int bits,
-                                                         int8_t *__restrict__ values, float *__restrict__ scales,
-                                                         float *__restrict__ offsets, int stride) {
-    pdl_enter();
-    const int groups = cols / 128;
-    const long long gw = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    const int lane = threadIdx.x & 31;
-    if (gw >= (long long)tokens * groups) return;
-    const int t = (int)(gw / groups), g = (int)(gw - (long long)t * groups);
-    const float *src = x + (size_t)t * cols + (size_t)g * 128;
-    float v[4];
-#pragma unroll
-    for (int k = 0; k < 4; k++) v[k] = src[lane + 32 * k];
+// Scalar.Hadamard's butterflies (src/Needle/Scalar.cs:76-89) on a warp's
+// 128 values, lane l holding elements l, l+32, l+64, l+96: strides 1, 2, ...,
+// 64 in that order, lower index a + b, upper a - b; strides below 32 across
+// lanes.  The 1/sqrt(128) scale is left to the caller.
+__device__ __forceinline__ void cq_fwht128(float (&v)[4], int lane) {
 #pragma unroll
     for (int s = 1; s < 32; s <<= 1) {
         const bool upper = (lane & s) != 0;
@@ -68,6 +57,23 @@ __global__ void __launch_bounds__(256) cq_prepare_kernel(const float *__restrict
         v[1] = __fadd_rn(a1, b1);
         v[3] = __fsub_rn(a1, b1);
     }
+}
+
+// Warp per (token, group); lane l holds elements l, l+32, l+64, l+96.
+__global__ void __launch_bounds__(256) cq_prepare_kernel(const float *__restrict__ x, int tokens, int cols, int bits,
+                                                         int8_t *__restrict__ values, float *__restrict__ scales,
+                                                         float *__restrict__ offsets, int stride) {
+    pdl_enter();
+    const int groups = cols / 128;
+    const long long gw = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (gw >= (long long)tokens * groups) return;
+    const int t = (int)(gw / groups), g = (int)(gw - (long long)t * groups);
+    const float *src = x + (size_t)t * cols + (size_t)g * 128;
+    float v[4];
+#pragma unroll
+    for (int k = 0; k < 4; k++) v[k] = src[lane + 32 * k];
+    cq_fwht128(v, lane);
     float peak = 0.0f;
 #pragma unroll
     for (int k = 0; k < 4; k++) {
@@ -306,6 +312,56 @@ __global__ void __launch_bounds__(32 * kCqWarps, 2) cq_matmul_kernel(
     }
 }
 
+// Quant.GatherRow (src/Needle/Quant.cs:566-576): a CQ row decoded to floats
+// (Scalar.DecodeRow, src/Needle/Scalar.cs:130-144: levels[index] * norm in
+// natural column order) and rotated back per 128-column group
+// (Scalar.Hadamard).  Warp per (output row, group); out[r] = row rows[r].
+struct CqLevels {
+    float v[16];
+};
+__global__ void __launch_bounds__(256) cq_gather_kernel(const uint8_t *__restrict__ indices,
+                                                        const uint16_t *__restrict__ norms, CqLevels levels, int rows,
+                                                        int cols, int bits, const int32_t *__restrict__ row_ids, int n,
+                                                        float *__restrict__ out, int *status) {
+    pdl_enter();
+    const int groups = cols / 128;
+    const long long gw = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (gw >= (long long)n * groups) return;
+    const int r = (int)(gw / groups), g = (int)(gw - (long long)r * groups);
+    const int row = row_ids[r];
+    float *dst = out + (size_t)r * cols + (size_t)g * 128;
+    if (row < 0 || row >= rows) {  // checked on the host for the C entry points; zeros and a status bit here
+        for (int k = 0; k < 4; k++) dst[lane + 32 * k] = 0.0f;
+        if (lane == 0 && status) atomicOr(status, 2);
+        return;
+    }
+    const size_t row_bytes = (size_t)cols * bits / 8;
+    const uint8_t *packed = indices + (size_t)row * row_bytes + (size_t)g * (bits == 2 ? 32 : 64);
+    const float norm = half_to_float_ref(norms[(size_t)row * groups + g]);
+    float v[4];
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        const int e = lane + 32 * k;
+        const int code = bits == 2 ? (packed[e >> 2] >> ((e & 3) * 2)) & 3 : (packed[e >> 1] >> ((e & 1) * 4)) & 15;
+        v[k] = __fmul_rn(levels.v[code], norm);
+    }
+    cq_fwht128(v, lane);
+#pragma unroll
+    for (int k = 0; k < 4; k++) dst[lane + 32 * k] = __fmul_rn(v[k], kCqHadamardScale);
+}
+
+int launch_cq_gather(const uint8_t *indices, const uint16_t *norms, const float *levels16, int rows, int cols, int bits,
+                     const int32_t *row_ids, int n, float *out, int *status, cudaStream_t stream) {
+    if (n == 0) return NDL_OK;
+    CqLevels lv;
+    memcpy(lv.v, levels16, sizeof(lv.v));
+    const long long warps = (long long)n * (cols / 128);
+    launch_kernel(cq_gather_kernel, dim3((unsigned)((warps + 7) / 8)), dim3(256), 0, stream, indices, norms, lv, rows,
+                  cols, bits, row_ids, n, out, status);
+    return check_launch("cq_gather");
+}
+
 int launch_cq_prepare(const float *x, int tokens, int cols, int bits, int8_t *values, float *scales, float *offsets,
                       int stride, cudaStream_t stream) {
     if (tokens == 0) return NDL_OK;
@@ -397,4 +453,13 @@ extern "C" NDL_API int ndl_cq_matmul(const uint8_t *indices, const uint16_t *nor
     NDL_REQUIRE(aligned(indices, 4) && aligned(values, 16), "indices need 4-byte, values 16-byte alignment");
     return launch_cq_matmul(indices, norms, book_bytes, byte_scale, cols, bits, values, scales, offsets, stride, tokens,
                             y, ldy, row_start, row_end, (cudaStream_t)stream);
+}
+
+extern "C" NDL_API int ndl_cq_gather_rows(const uint8_t *indices, const uint16_t *norms, const float *levels, int rows,
+                                          int cols, int bits, const int32_t *row_ids, int n, float *out, void *stream) {
+    NDL_REQUIRE(cols >= 128 && cols % 128 == 0 && rows >= 1 && n >= 0, "rows %d / cols %d / n %d", rows, cols, n);
+    NDL_REQUIRE(bits == 2 || bits == 4, "bits %d (2 or 4)", bits);
+    if (n == 0) return NDL_OK;
+    NDL_REQUIRE(indices && norms && levels && row_ids && out, "null pointer");
+    return launch_cq_gather(indices, norms, levels, rows, cols, bits, row_ids, n, out, nullptr, (cudaStream_t)stream);
 }

@@ -284,6 +284,25 @@ void ndo_prepare_cq(const float *x, int tokens, int cols, int bits, int8_t *valu
         }
 }
 
+/* Quant.GatherRow scalar path (src/Needle/Quant.cs:566-576): Scalar.DecodeRow
+ * (src/Needle/Scalar.cs:130-144), levels[index] * norm in natural column
+ * order, then Scalar.Hadamard in place per 128-column group. */
+void ndo_gather_row_cq(const uint8_t *indices, const uint16_t *norms, const float *levels, int cols, int bits, int row,
+                       float *dst) {
+    int groups = cols / 128;
+    int row_bytes = cols * bits / 8;
+    const uint8_t *idx = indices + (size_t)row * row_bytes;
+    const uint16_t *nr = norms + (size_t)row * groups;
+    for (int g = 0; g < groups; g++) {
+        float norm = ndo_half_to_single(nr[g]);
+        float *d = dst + g * 128;
+        for (int i = 0; i < 128; i++)
+            d[i] = bits == 2 ? levels[idx[g * 32 + i / 4] >> (i % 4 * 2) & 3] * norm
+                             : levels[idx[g * 64 + i / 2] >> (i % 2 * 4) & 15] * norm;
+        ndo_hadamard128(d, d);
+    }
+}
+
 /* Scalar.MatMulRows (src/Needle/Scalar.cs:146-192). */
 void ndo_matmul_rows_cq(const uint8_t *indices, const uint16_t *norms, const ndo_codebook *book, int rows,
                         int cols, int bits, const int8_t *values, const float *scales, const float *offsets,

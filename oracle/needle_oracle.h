@@ -58,6 +58,8 @@ typedef struct {
     float byte_scale;
 } ndo_codebook;
 void ndo_codebook_fill(ndo_codebook *book, const float *levels, int count);
+void ndo_gather_row_cq(const uint8_t *indices, const uint16_t *norms, const float *levels, int cols, int bits, int row,
+                       float *dst); /* Quant.cs:566-576 */
 
 /* CQ activations prepare, scalar branch (src/Needle/Quant.cs:471-484). */
 void ndo_prepare_cq(const float *x, int tokens, int cols, int bits, int8_t *values, float *scales,

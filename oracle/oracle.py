@@ -45,6 +45,7 @@ _SIGS = {
     "ndo_codebook_fill": (None, [P, P, I]),
     "ndo_prepare_cq": (None, [P, I, I, I, P, P, P, I]),
     "ndo_matmul_rows_cq": (None, [P, P, P, I, I, I, P, P, P, I, I, P, I, I, I]),
+    "ndo_gather_row_cq": (None, [P, P, P, I, I, I, P]),
     "ndo_matmul_i8g32": (None, [P, P, I, I, P, P, I, P, P, I]),
     "ndo_attention_head": (None, [P, F, P, P, P, P, I, I, I, I, I, I, I, F, P, P, P]),
     "ndo_merge_partials": (None, [P, I, I, I, I, P]),
@@ -188,6 +189,17 @@ def matmul_rows_cq(indices, norms, book, bits, vals, sc, off, row_start=0, row_e
     lib().ndo_matmul_rows_cq(ptr(indices), ptr(norms), _c.byref(book), rows, cols, bits, ptr(vals), ptr(sc),
                              ptr(off), sc.shape[1], tokens, ptr(y), y.shape[1], row_start, row_end)
     return y
+
+
+def gather_row_cq(indices, norms, levels, bits, row):
+    """Quant.GatherRow: CQ row `row` decoded and rotated back per group."""
+    indices = np.ascontiguousarray(indices, np.uint8)
+    norms = np.ascontiguousarray(norms, np.uint16)
+    cols = indices.shape[1] * 8 // bits
+    out = np.empty(cols, np.float32)
+    lib().ndo_gather_row_cq(ptr(indices), ptr(norms), ptr(f32(np.resize(np.asarray(levels, np.float32), 16))), cols,
+                            bits, row, ptr(out))
+    return out
 
 
 def rms_norm(x, w):

@@ -167,3 +167,37 @@ def test_device_entry_points(pkg, oracle):
                      100, bits, dv.data_ptr(), ds.data_ptr(), do.data_ptr(), stride, tokens, dy.data_ptr(), rows, 0,
                      rows, None)
     assert e.value.status == 100
+
+
+@pytest.mark.parametrize("bits,rows,cols", [(2, 6, 128), (4, 9, 768), (2, 300, 2048), (4, 33, 4096)])
+def test_gather_row_matches_oracle(lib, oracle, bits, rows, cols):
+    """GatherRow (slot 2) and the batched device entry point equal the oracle's
+    DecodeRow + Hadamard bit for bit."""
+    import torch
+
+    from needle_cs_b200 import _native
+
+    lib.ndl_kt_gather_row.restype = None
+    lib.ndl_kt_gather_row.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]
+    book, idx, norms = _weights(oracle, 0x4321 + rows, bits, rows, cols)
+    levels = np.frombuffer(bytes(book)[:64], np.float32)
+    kbook = KtCodebook.from_buffer_copy(bytes(book))
+    w = KtCq(idx.ctypes.data, norms.ctypes.data, ctypes.addressof(kbook), rows, cols, bits)
+    picks = sorted({0, rows - 1, rows // 2, 1 % rows})
+    for row in picks:
+        got = np.full(cols, 7.0, np.float32)
+        lib.ndl_kt_gather_row(ctypes.byref(w), row, got.ctypes.data)
+        want = oracle.gather_row_cq(idx, norms, levels, bits, row)
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), row
+    dev = torch.device("cuda:0")
+    ids = np.array(picks[::-1] + picks, np.int32)  # reordered and repeated rows
+    di, dn = torch.from_numpy(idx).to(dev), torch.from_numpy(norms.view(np.int16)).to(dev)
+    dids = torch.from_numpy(ids).to(dev)
+    out = torch.zeros((ids.size, cols), dtype=torch.float32, device=dev)
+    lv = np.ascontiguousarray(levels)
+    _native.call("ndl_cq_gather_rows", di.data_ptr(), dn.data_ptr(), lv.ctypes.data, rows, cols, bits,
+                 dids.data_ptr(), ids.size, out.data_ptr(), None)
+    torch.cuda.synchronize()
+    got = out.cpu().numpy()
+    for r, row in enumerate(ids):
+        assert np.array_equal(got[r], oracle.gather_row_cq(idx, norms, levels, bits, int(row))), (r, row)

@@ -235,6 +235,30 @@ def test_i8g32_matches_numpy_int(oracle):
     assert np.allclose(y, ref, rtol=1e-5, atol=1e-5)
 
 
+@pytest.mark.parametrize("bits,cols", [(2, 128), (4, 384), (2, 768)])
+def test_cq_gather_row_matches_float(oracle, bits, cols):
+    """Quant.GatherRow (DecodeRow, then the scaled Walsh-Hadamard transform
+    per group) equals a float64 evaluation with the Sylvester matrix."""
+    rng = np.random.default_rng(bits * 1000 + cols)
+    rows, groups = 3, cols // 128
+    idx = rng.integers(0, 256, (rows, cols * bits // 8), dtype=np.uint8)
+    norms = np.float16(rng.uniform(0.2, 2.0, (rows, groups))).view(np.uint16)
+    levels = np.linspace(-1.0, 1.0, 16).astype(np.float32)
+    h = np.array([[1.0]])
+    while h.shape[0] < 128:
+        h = np.block([[h, h], [h, -h]])
+    for row in range(rows):
+        got = oracle.gather_row_cq(idx, norms, levels, bits, row)
+        if bits == 2:
+            codes = np.stack([(idx[row] >> (2 * p)) & 3 for p in range(4)], 1).reshape(-1)
+        else:
+            codes = np.stack([idx[row] & 15, idx[row] >> 4], 1).reshape(-1)
+        dec = levels[codes].astype(np.float64).reshape(groups, 128) * \
+            norms[row].view(np.float16).astype(np.float64)[:, None]
+        want = (dec @ h.T * 0.08838834764831845).reshape(-1)
+        assert np.allclose(got, want, rtol=1e-5, atol=1e-5)
+
+
 @pytest.mark.parametrize("bits,rows,cols,tokens", [(2, 4, 128, 2), (4, 4, 128, 2), (2, 5, 768, 3), (4, 7, 384, 5)])
 def test_cq_matmul_matches_dequantized_float(oracle, bits, rows, cols, tokens):
     """Scalar.MatMulRows on ConformanceWeights-style CQ inputs equals a
