@@ -224,7 +224,7 @@ class CqWorkload:
 
     name = "cq_linear"
     metric = "CQ linear GB/s (algorithmic bytes)"
-    kernel = "cq_matmul_kernel<2> (codebook byte permutes + dp4a)"
+    kernel = "cq_matmul_kernel<2> (codebook byte permutes into mma.sync s8 fragments)"
     dtype = "u2 codes x int8 -> int32, f32"
 
     def __init__(self, m=16, n=2048, k=512, bits=2, copies=768):
