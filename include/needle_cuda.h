@@ -241,6 +241,31 @@ NDL_API void ndl_kt_prepare(const float *x, int tokens, int cols, int bits, cons
  * per 128-column group (Scalar.Hadamard), bit for bit. */
 NDL_API void ndl_kt_gather_row(const ndl_kt_cq *w, int row, float *destination);
 
+/* The Needle-3 row slots, same conventions (Scalar.cs:250-439, Ops.cs:800-812):
+ *   RmsFakeA8          void(float* x, int n, float* destination)              slot 6
+ *   CenteredRmsFakeA8  void(float* x, float* scale, int n, float* destination) slot 7
+ *   GateFakeA8         void(float* x, float* gate, int n)                      slot 8 (x in place)
+ *   PostNormAdd        void(float* residual, float* x, float* scale, float gate, int n)  slot 9
+ *   CombineDiff4       void(float* s, int dim, float w0..w3, float* x, float* u, float post, float* destination) slot 10
+ *   Mix4               void(float* s, int dim, float w0..w3, float* destination)  slot 11
+ *   Combine4           void(float* s, int dim, float w0..w3, float* y, float post, float* destination) slot 12
+ *   Taps3              void(float* taps, int width, float* current, float* destination) slot 13
+ *                      (reads current[-2*width .. width))
+ *   Sinkhorn4x4        void(float* logits, float* result)                      slot 24
+ * Equal to the scalar code bit for bit except GateFakeA8 and Sinkhorn4x4,
+ * whose exp is CUDA's expf (tolerance). */
+NDL_API void ndl_kt_rms_fake_a8(const float *x, int n, float *destination);
+NDL_API void ndl_kt_centered_rms_fake_a8(const float *x, const float *scale, int n, float *destination);
+NDL_API void ndl_kt_gate_fake_a8(float *x, const float *gate, int n);
+NDL_API void ndl_kt_post_norm_add(float *residual, const float *x, const float *scale, float gate, int n);
+NDL_API void ndl_kt_combine_diff4(const float *s, int dim, float w0, float w1, float w2, float w3, const float *x,
+                                  const float *u, float post, float *destination);
+NDL_API void ndl_kt_mix4(const float *s, int dim, float w0, float w1, float w2, float w3, float *destination);
+NDL_API void ndl_kt_combine4(const float *s, int dim, float w0, float w1, float w2, float w3, const float *y,
+                             float post, float *destination);
+NDL_API void ndl_kt_taps3(const float *taps, int width, const float *current, float *destination);
+NDL_API void ndl_kt_sinkhorn4x4(const float *logits, float *result);
+
 /* The same two operations on device memory, stream-ordered: CQ activation
  * prep for `tokens` rows of x [tokens][cols] (values [tokens][cols], scales
  * and offsets [tokens][stride]) and the CQ matmul y[t*ldy + n] for n in
@@ -259,6 +284,27 @@ NDL_API int ndl_cq_matmul(const uint8_t *indices, const uint16_t *norms, const u
  * row of zeros: ids are device data, so check them where they are made. */
 NDL_API int ndl_cq_gather_rows(const uint8_t *indices, const uint16_t *norms, const float *levels, int rows, int cols,
                                int bits, const int32_t *row_ids, int n, float *out, void *stream);
+
+/* The same row operations batched over n tokens on device memory (a Needle-3
+ * layer, EngineCore.RunLayerBatch, src/Needle/Engine.cs:2352-2404):
+ *   hc_mix4           dst[t] = sum_i w[t][i] * s[t][i]       s [n][4][dim], w [n][4]
+ *   hc_combine4       dst[t] = post[t] * y[t] + sum_i w[t][i] * s[t][i]
+ *   hc_combine_diff4x4  stream o of dst[t] = post_gate[t][o] * (x[t] - u[t])
+ *                     + sum_i mix[t][4o + i] * s[t][i]          dst [n][4][dim]
+ *   hc_sinkhorn4x4    out[t] = Sinkhorn4x4(logits[t])        [n][16]
+ *   taps3             dst[t] = Taps3 over triples[t] = (x_{t-2}, x_{t-1}, x_t)  [n][3][width]
+ *   fake_a8_rows      mode 0 RmsFakeA8, 1 CenteredRmsFakeA8 (aux = scale [n]),
+ *                     2 GateFakeA8 (aux = gates [rows][n]), 3 PostNormAdd
+ *                     (aux = scale [n], gate [rows], dst = residual, updated). */
+NDL_API int ndl_hc_mix4(const float *s, int dim, const float *w, int n, float *dst, void *stream);
+NDL_API int ndl_hc_combine4(const float *s, int dim, const float *w, const float *y, const float *post, int n,
+                            float *dst, void *stream);
+NDL_API int ndl_hc_combine_diff4x4(const float *s, int dim, const float *mix, const float *x, const float *u,
+                                   const float *post_gate, int n, float *dst, void *stream);
+NDL_API int ndl_hc_sinkhorn4x4(const float *logits, int n, float *out, void *stream);
+NDL_API int ndl_taps3(const float *taps, int width, const float *triples, int n, float *dst, void *stream);
+NDL_API int ndl_fake_a8_rows(int mode, const float *x, const float *aux, const float *gate, int rows, int n,
+                             float *dst, void *stream);
 
 /* ------------------------------------------------------------------ */
 /* Batched decode engine (replaces BatchedEngine + EngineCore slots)   */

@@ -83,6 +83,21 @@ SIGNATURES = {
     "ndl_kt_matmul_rows": (None, [c_void_p, c_void_p, c_int, c_void_p, c_int, c_int, c_int]),
     "ndl_kt_prepare": (None, [c_void_p, c_int, c_int, c_int, c_void_p]),
     "ndl_kt_gather_row": (None, [c_void_p, c_int, c_void_p]),
+    "ndl_kt_rms_fake_a8": (None, [c_void_p, c_int, c_void_p]),
+    "ndl_kt_centered_rms_fake_a8": (None, [c_void_p, c_void_p, c_int, c_void_p]),
+    "ndl_kt_gate_fake_a8": (None, [c_void_p, c_void_p, c_int]),
+    "ndl_kt_post_norm_add": (None, [c_void_p, c_void_p, c_void_p, c_float, c_int]),
+    "ndl_kt_combine_diff4": (None, [c_void_p, c_int, c_float, c_float, c_float, c_float, c_void_p, c_void_p, c_float, c_void_p]),
+    "ndl_kt_mix4": (None, [c_void_p, c_int, c_float, c_float, c_float, c_float, c_void_p]),
+    "ndl_kt_combine4": (None, [c_void_p, c_int, c_float, c_float, c_float, c_float, c_void_p, c_float, c_void_p]),
+    "ndl_kt_taps3": (None, [c_void_p, c_int, c_void_p, c_void_p]),
+    "ndl_kt_sinkhorn4x4": (None, [c_void_p, c_void_p]),
+    "ndl_hc_mix4": (c_int, [c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p]),
+    "ndl_hc_combine4": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_void_p]),
+    "ndl_hc_combine_diff4x4": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_void_p]),
+    "ndl_hc_sinkhorn4x4": (c_int, [c_void_p, c_int, c_void_p, c_void_p]),
+    "ndl_taps3": (c_int, [c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p]),
+    "ndl_fake_a8_rows": (c_int, [c_int, c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p]),
     "ndl_beam_search": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_void_p,
                                 c_void_p, c_void_p]),
     "ndl_sched_create": (c_int, [c_void_p, c_void_p, c_void_p]),

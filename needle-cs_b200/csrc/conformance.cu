@@ -6,7 +6,10 @@
 // kernels.  Like the slots they replace they have no error channel: a CUDA
 // failure returns NaN (scales, probabilities) or -2 (argmax) and leaves the
 // reason in ndl_last_error.
+#include <initializer_list>
 #include <mutex>
+#include <utility>
+#include <vector>
 
 #include "common.cuh"
 #include "kernels.cuh"
@@ -25,6 +28,13 @@ int launch_cq_matmul(const uint8_t *indices, const uint16_t *norms, const uint8_
                      int tokens, float *y, int ldy, int row_start, int row_end, cudaStream_t stream);
 int launch_cq_gather(const uint8_t *indices, const uint16_t *norms, const float *levels16, int rows, int cols, int bits,
                      const int32_t *row_ids, int n, float *out, int *status, cudaStream_t stream);
+int launch_mix4(const float *s, int dim, const float *w, int n, float *dst, cudaStream_t stream);
+int launch_combine4(bool diff, const float *s, int dim, const float *mix, const float *x, const float *u,
+                    const float *post, int n, float *dst, cudaStream_t stream);
+int launch_sinkhorn4x4(const float *logits, int n, float *out, cudaStream_t stream);
+int launch_taps3(const float *taps, int width, const float *triples, int n, float *dst, cudaStream_t stream);
+int launch_fake_a8(int mode, const float *x, const float *aux, const float *gate, int rows, int n, float *dst,
+                   cudaStream_t stream);
 }  // namespace ndl
 
 namespace {
@@ -58,6 +68,39 @@ int scratch(size_t bytes, void **out) {
 }
 
 size_t align16(size_t n) { return (n + 15) & ~size_t(15); }
+
+// Host float arrays in, one launch, host float arrays out, through the
+// scratch buffer: in[k] (n_in[k] floats) go up, the launch gets their device
+// copies (ins) and the outputs' (outs), outputs come back.
+template <typename F>
+bool run_floats(const char *what, std::initializer_list<std::pair<const float *, size_t>> in,
+                std::initializer_list<std::pair<float *, size_t>> out, F launch) {
+    size_t bytes = 0;
+    for (auto &a : in) bytes += align16(a.second * 4);
+    for (auto &a : out) bytes += align16(a.second * 4);
+    void *buf = nullptr;
+    if (scratch(bytes + 16, &buf) != NDL_OK) return false;
+    char *p = static_cast<char *>(buf);
+    std::vector<float *> ins, outs;
+    bool ok = true;
+    for (auto &a : in) {
+        ins.push_back(reinterpret_cast<float *>(p));
+        ok = ok && cudaMemcpy(p, a.first, a.second * 4, cudaMemcpyHostToDevice) == cudaSuccess;
+        p += align16(a.second * 4);
+    }
+    for (auto &a : out) {
+        outs.push_back(reinterpret_cast<float *>(p));
+        p += align16(a.second * 4);
+    }
+    ok = ok && launch(ins, outs) == NDL_OK;
+    size_t k = 0;
+    for (auto &a : out) ok = ok && cudaMemcpy(a.first, outs[k++], a.second * 4, cudaMemcpyDeviceToHost) == cudaSuccess;
+    if (!ok) {
+        cudaGetLastError();
+        set_error(NDL_ERR_CUDA, "%s failed", what);
+    }
+    return ok;
+}
 
 }  // namespace
 
@@ -237,6 +280,90 @@ NDL_API void ndl_kt_gather_row(const ndl_kt_cq *w, int row, float *destination) 
         cudaGetLastError();
         set_error(NDL_ERR_CUDA, "gather_row failed");
     }
+}
+
+
+// The Needle-3 row slots (Scalar.cs:250-439): 6 RmsFakeA8, 7 CenteredRmsFakeA8,
+// 8 GateFakeA8, 9 PostNormAdd, 10 CombineDiff4, 11 Mix4, 12 Combine4,
+// 13 Taps3, 24 Sinkhorn4x4.
+NDL_API void ndl_kt_rms_fake_a8(const float *x, int n, float *destination) {
+    std::lock_guard<std::mutex> lock(g_mu);
+    if (!x || !destination || n < 1) return (void)set_error(NDL_ERR_INVALID_ARG, "rms_fake_a8: bad arguments");
+    run_floats("rms_fake_a8", {{x, (size_t)n}}, {{destination, (size_t)n}},
+               [&](auto &i, auto &o) { return launch_fake_a8(0, i[0], nullptr, nullptr, 1, n, o[0], nullptr); });
+}
+
+NDL_API void ndl_kt_centered_rms_fake_a8(const float *x, const float *scale, int n, float *destination) {
+    std::lock_guard<std::mutex> lock(g_mu);
+    if (!x || !scale || !destination || n < 1)
+        return (void)set_error(NDL_ERR_INVALID_ARG, "centered_rms_fake_a8: bad arguments");
+    run_floats("centered_rms_fake_a8", {{x, (size_t)n}, {scale, (size_t)n}}, {{destination, (size_t)n}},
+               [&](auto &i, auto &o) { return launch_fake_a8(1, i[0], i[1], nullptr, 1, n, o[0], nullptr); });
+}
+
+NDL_API void ndl_kt_gate_fake_a8(float *x, const float *gate, int n) {
+    std::lock_guard<std::mutex> lock(g_mu);
+    if (!x || !gate || n < 1) return (void)set_error(NDL_ERR_INVALID_ARG, "gate_fake_a8: bad arguments");
+    run_floats("gate_fake_a8", {{x, (size_t)n}, {gate, (size_t)n}}, {{x, (size_t)n}},
+               [&](auto &i, auto &o) { return launch_fake_a8(2, i[0], i[1], nullptr, 1, n, o[0], nullptr); });
+}
+
+NDL_API void ndl_kt_post_norm_add(float *residual, const float *x, const float *scale, float gate, int n) {
+    std::lock_guard<std::mutex> lock(g_mu);
+    if (!residual || !x || !scale || n < 1) return (void)set_error(NDL_ERR_INVALID_ARG, "post_norm_add: bad arguments");
+    run_floats("post_norm_add", {{x, (size_t)n}, {scale, (size_t)n}, {&gate, 1}, {residual, (size_t)n}},
+               {{residual, (size_t)n}}, [&](auto &i, auto &o) -> int {
+                   if (cudaMemcpy(o[0], i[3], (size_t)n * 4, cudaMemcpyDeviceToDevice) != cudaSuccess)
+                       return (int)NDL_ERR_CUDA;
+                   return launch_fake_a8(3, i[0], i[1], i[2], 1, n, o[0], nullptr);
+               });
+}
+
+NDL_API void ndl_kt_combine_diff4(const float *s, int dim, float w0, float w1, float w2, float w3, const float *x,
+                                  const float *u, float post, float *destination) {
+    std::lock_guard<std::mutex> lock(g_mu);
+    if (!s || !x || !u || !destination || dim < 1)
+        return (void)set_error(NDL_ERR_INVALID_ARG, "combine_diff4: bad arguments");
+    const float mix[16] = {w0, w1, w2, w3};  // stream 0 is the slot's; streams 1-3 are discarded
+    const float gates[4] = {post, 0.0f, 0.0f, 0.0f};
+    std::vector<float> all((size_t)4 * dim);
+    if (run_floats("combine_diff4", {{s, (size_t)4 * dim}, {mix, 16}, {x, (size_t)dim}, {u, (size_t)dim}, {gates, 4}},
+                   {{all.data(), all.size()}}, [&](auto &i, auto &o) {
+                       return launch_combine4(true, i[0], dim, i[1], i[2], i[3], i[4], 1, o[0], nullptr);
+                   }))
+        memcpy(destination, all.data(), (size_t)dim * 4);
+}
+
+NDL_API void ndl_kt_mix4(const float *s, int dim, float w0, float w1, float w2, float w3, float *destination) {
+    std::lock_guard<std::mutex> lock(g_mu);
+    if (!s || !destination || dim < 1) return (void)set_error(NDL_ERR_INVALID_ARG, "mix4: bad arguments");
+    const float w[4] = {w0, w1, w2, w3};
+    run_floats("mix4", {{s, (size_t)4 * dim}, {w, 4}}, {{destination, (size_t)dim}},
+               [&](auto &i, auto &o) { return launch_mix4(i[0], dim, i[1], 1, o[0], nullptr); });
+}
+
+NDL_API void ndl_kt_combine4(const float *s, int dim, float w0, float w1, float w2, float w3, const float *y,
+                             float post, float *destination) {
+    std::lock_guard<std::mutex> lock(g_mu);
+    if (!s || !y || !destination || dim < 1) return (void)set_error(NDL_ERR_INVALID_ARG, "combine4: bad arguments");
+    const float w[4] = {w0, w1, w2, w3};
+    run_floats("combine4", {{s, (size_t)4 * dim}, {w, 4}, {y, (size_t)dim}, {&post, 1}}, {{destination, (size_t)dim}},
+               [&](auto &i, auto &o) { return launch_combine4(false, i[0], dim, i[1], i[2], nullptr, i[3], 1, o[0], nullptr); });
+}
+
+NDL_API void ndl_kt_taps3(const float *taps, int width, const float *current, float *destination) {
+    std::lock_guard<std::mutex> lock(g_mu);
+    if (!taps || !current || !destination || width < 1) return (void)set_error(NDL_ERR_INVALID_ARG, "taps3: bad arguments");
+    run_floats("taps3", {{taps, (size_t)3 * width}, {current - 2 * (size_t)width, (size_t)3 * width}},
+               {{destination, (size_t)width}},
+               [&](auto &i, auto &o) { return launch_taps3(i[0], width, i[1], 1, o[0], nullptr); });
+}
+
+NDL_API void ndl_kt_sinkhorn4x4(const float *logits, float *result) {
+    std::lock_guard<std::mutex> lock(g_mu);
+    if (!logits || !result) return (void)set_error(NDL_ERR_INVALID_ARG, "sinkhorn4x4: bad arguments");
+    run_floats("sinkhorn4x4", {{logits, 16}}, {{result, 16}},
+               [&](auto &i, auto &o) { return launch_sinkhorn4x4(i[0], 1, o[0], nullptr); });
 }
 
 }  // extern "C"

@@ -1,0 +1,253 @@
+// Needle-3 row operations around a layer (the reference's hyper-connection
+// streams, conv taps and fake-A8 norms), batched over tokens on the device.
+//
+// Hyper-connections (EngineCore.RunLayerBatch, src/Needle/Engine.cs:2352-2404):
+// a token carries 4 streams of `dim` floats.  Before the layer the streams
+// mix into the layer input (Mix4, Scalar.cs:255-258) and a 4x4 Sinkhorn
+// matrix (Scalar.Sinkhorn4x4, Scalar.cs:360-379) is made from the layer's
+// logits; after it, CombineDiff4x4 (Ops.cs:800-812) forms the next streams.
+// Conv taps: Scalar.Taps3 (Scalar.cs:285-288) over a (t-2, t-1, t) triple
+// (EngineCore.ChainTriple, Engine.cs:2471-2478).  Fake-A8 norms:
+// Scalar.RmsFakeA8 / CenteredRmsFakeA8 / GateFakeA8 / PostNormAdd
+// (Scalar.cs:381-439).
+//
+// The arithmetic follows the scalar code term by term (no contraction; sums
+// of squares in ascending order on one lane), so every result except those
+// through exp equals the scalar restatement bit for bit.
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace ndl {
+
+__device__ __forceinline__ float mix4_term(float acc, float w0, float w1, float w2, float w3, const float *s, int dim,
+                                           int c) {
+    acc = __fadd_rn(acc, __fmul_rn(w0, s[c]));
+    acc = __fadd_rn(acc, __fmul_rn(w1, s[dim + c]));
+    acc = __fadd_rn(acc, __fmul_rn(w2, s[2 * dim + c]));
+    return __fadd_rn(acc, __fmul_rn(w3, s[3 * dim + c]));
+}
+
+// Mix4 per token: dst[t] = sum_i w[t][i] * s[t][i] (s [n][4][dim]).
+__global__ void __launch_bounds__(256) mix4_kernel(const float *__restrict__ s, int dim, const float *__restrict__ w,
+                                                   int n, float *__restrict__ dst) {
+    pdl_enter();
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (long long)n * dim) return;
+    const int t = (int)(i / dim), c = (int)(i - (long long)t * dim);
+    const float *st = s + (size_t)t * 4 * dim, *wt = w + (size_t)t * 4;
+    const float first = __fmul_rn(wt[0], st[c]);
+    float acc = __fadd_rn(first, __fmul_rn(wt[1], st[dim + c]));
+    acc = __fadd_rn(acc, __fmul_rn(wt[2], st[2 * dim + c]));
+    dst[(size_t)t * dim + c] = __fadd_rn(acc, __fmul_rn(wt[3], st[3 * dim + c]));
+}
+
+// CombineDiff4x4 per token: stream i of dst[t] = post[t][i] * (x - u)
+// + sum_j mix[t][4i + j] * s[t][j]; with kDiff false, Combine4 per token
+// (x as y, u unused, one output stream).
+template <bool kDiff>
+__global__ void __launch_bounds__(256) combine4_kernel(const float *__restrict__ s, int dim,
+                                                       const float *__restrict__ mix, const float *__restrict__ x,
+                                                       const float *__restrict__ u, const float *__restrict__ post,
+                                                       int n, float *__restrict__ dst) {
+    pdl_enter();
+    constexpr int kOut = kDiff ? 4 : 1;
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (long long)n * kOut * dim) return;
+    const int t = (int)(i / (kOut * dim));
+    const int rest = (int)(i - (long long)t * kOut * dim), o = rest / dim, c = rest - o * dim;
+    const float *st = s + (size_t)t * 4 * dim, *m = mix + (size_t)t * (kDiff ? 16 : 4) + 4 * o;
+    const float xv = x[(size_t)t * dim + c];
+    const float head = kDiff ? __fmul_rn(post[(size_t)t * 4 + o], __fsub_rn(xv, u[(size_t)t * dim + c]))
+                             : __fmul_rn(post[t], xv);
+    dst[((size_t)t * kOut + o) * dim + c] = mix4_term(head, m[0], m[1], m[2], m[3], st, dim, c);
+}
+
+// Sinkhorn4x4 per token, one thread each.
+__global__ void __launch_bounds__(128) sinkhorn4x4_kernel(const float *__restrict__ logits, int n,
+                                                          float *__restrict__ out) {
+    pdl_enter();
+    const int t = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= n) return;
+    const float *lg = logits + (size_t)t * 16;
+    float r[16];
+#pragma unroll
+    for (int row = 0; row < 4; row++) {
+        const float peak = fmaxf(fmaxf(lg[row * 4], lg[row * 4 + 1]), fmaxf(lg[row * 4 + 2], lg[row * 4 + 3]));
+#pragma unroll
+        for (int c = 0; c < 4; c++) r[row * 4 + c] = expf(__fsub_rn(lg[row * 4 + c], peak));
+    }
+    for (int it = 0; it < 20; it++) {
+#pragma unroll
+        for (int row = 0; row < 4; row++) {
+            const float sum = __fadd_rn(__fadd_rn(__fadd_rn(r[row * 4], r[row * 4 + 1]), r[row * 4 + 2]), r[row * 4 + 3]);
+#pragma unroll
+            for (int c = 0; c < 4; c++) r[row * 4 + c] = __fdiv_rn(r[row * 4 + c], sum);
+        }
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+            const float sum = __fadd_rn(__fadd_rn(__fadd_rn(r[c], r[4 + c]), r[8 + c]), r[12 + c]);
+            if (sum > 0.0f)
+#pragma unroll
+                for (int row = 0; row < 4; row++) r[row * 4 + c] = __fdiv_rn(r[row * 4 + c], sum);
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < 16; k++) out[(size_t)t * 16 + k] = r[k];
+}
+
+// Taps3 on triples [n][3][width] = (x_{t-2}, x_{t-1}, x_t).
+__global__ void __launch_bounds__(256) taps3_kernel(const float *__restrict__ taps, int width,
+                                                    const float *__restrict__ triples, int n,
+                                                    float *__restrict__ dst) {
+    pdl_enter();
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (long long)n * width) return;
+    const int t = (int)(i / width), c = (int)(i - (long long)t * width);
+    const float *cur = triples + (size_t)t * 3 * width + 2 * width;
+    float acc = __fmul_rn(taps[c], cur[c]);
+    acc = __fadd_rn(acc, __fmul_rn(taps[width + c], cur[c - width]));
+    dst[(size_t)t * width + c] = __fadd_rn(acc, __fmul_rn(taps[2 * width + c], cur[c - 2 * width]));
+}
+
+// Warp per row.  MODE 0 RmsFakeA8, 1 CenteredRmsFakeA8 (aux = scale),
+// 2 GateFakeA8 (aux = gate), 3 PostNormAdd (aux = scale, dst = residual,
+// gate[row]).  The sum of squares runs on lane 0 in ascending order.
+template <int MODE>
+__global__ void __launch_bounds__(256) fake_a8_kernel(const float *__restrict__ x, const float *__restrict__ aux,
+                                                      const float *__restrict__ gate, int rows, int n,
+                                                      float *__restrict__ dst) {
+    pdl_enter();
+    const int row = (int)(((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    const float *xr = x + (size_t)row * n;
+    float *dr = dst + (size_t)row * n;
+    float inverse = 0.0f;
+    if (MODE != 2) {
+        float sum = 0.0f;
+        if (lane == 0)
+            for (int i = 0; i < n; i++) sum = __fadd_rn(sum, __fmul_rn(xr[i], xr[i]));
+        sum = __shfl_sync(0xffffffffu, sum, 0);
+        inverse = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, (float)n), 1e-6f)));
+    }
+    if (MODE == 3) {
+        const float g = gate[row];
+        for (int i = lane; i < n; i += 32)
+            dr[i] = __fadd_rn(dr[i], __fmul_rn(g, __fmul_rn(__fmul_rn(__fadd_rn(1.0f, aux[i]), xr[i]), inverse)));
+        return;
+    }
+    float peak = 0.0f;
+    for (int i = lane; i < n; i += 32) {
+        float v;
+        if (MODE == 0) v = __fmul_rn(xr[i], inverse);
+        else if (MODE == 1) v = __fmul_rn(__fmul_rn(__fadd_rn(1.0f, aux[i]), xr[i]), inverse);
+        else v = __fmul_rn(xr[i], __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-aux[(size_t)row * n + i]))));
+        dr[i] = v;
+        peak = fmaxf(peak, fabsf(v));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) peak = fmaxf(peak, __shfl_xor_sync(0xffffffffu, peak, o));
+    const float scale = peak > 0.0f ? __fdiv_rn(peak, 127.0f) : 1.0f;
+    const float round = __fdiv_rn(1.0f, scale);
+    __syncwarp();
+    for (int i = lane; i < n; i += 32) {
+        // Scalar.RoundEven (Scalar.cs:52-53): x + 1.5*2^23 - 1.5*2^23, which also
+        // turns -0 into +0 (rintf would keep the sign of a zero)
+        const float r = __fsub_rn(__fadd_rn(__fmul_rn(dr[i], round), 12582912.0f), 12582912.0f);
+        dr[i] = __fmul_rn(fminf(fmaxf(r, -128.0f), 127.0f), scale);
+    }
+}
+
+static unsigned blocks_for(long long threads, int per_block) {
+    return (unsigned)((threads + per_block - 1) / per_block);
+}
+
+int launch_mix4(const float *s, int dim, const float *w, int n, float *dst, cudaStream_t stream) {
+    if (n == 0) return NDL_OK;
+    launch_kernel(mix4_kernel, dim3(blocks_for((long long)n * dim, 256)), dim3(256), 0, stream, s, dim, w, n, dst);
+    return check_launch("mix4");
+}
+int launch_combine4(bool diff, const float *s, int dim, const float *mix, const float *x, const float *u,
+                    const float *post, int n, float *dst, cudaStream_t stream) {
+    if (n == 0) return NDL_OK;
+    if (diff)
+        launch_kernel(combine4_kernel<true>, dim3(blocks_for((long long)n * 4 * dim, 256)), dim3(256), 0, stream, s,
+                      dim, mix, x, u, post, n, dst);
+    else
+        launch_kernel(combine4_kernel<false>, dim3(blocks_for((long long)n * dim, 256)), dim3(256), 0, stream, s, dim,
+                      mix, x, u, post, n, dst);
+    return check_launch("combine4");
+}
+int launch_sinkhorn4x4(const float *logits, int n, float *out, cudaStream_t stream) {
+    if (n == 0) return NDL_OK;
+    launch_kernel(sinkhorn4x4_kernel, dim3(blocks_for(n, 128)), dim3(128), 0, stream, logits, n, out);
+    return check_launch("sinkhorn4x4");
+}
+int launch_taps3(const float *taps, int width, const float *triples, int n, float *dst, cudaStream_t stream) {
+    if (n == 0) return NDL_OK;
+    launch_kernel(taps3_kernel, dim3(blocks_for((long long)n * width, 256)), dim3(256), 0, stream, taps, width,
+                  triples, n, dst);
+    return check_launch("taps3");
+}
+int launch_fake_a8(int mode, const float *x, const float *aux, const float *gate, int rows, int n, float *dst,
+                   cudaStream_t stream) {
+    if (rows == 0) return NDL_OK;
+    const dim3 grid(blocks_for((long long)rows * 32, 256)), block(256);
+    switch (mode) {
+        case 0: launch_kernel(fake_a8_kernel<0>, grid, block, 0, stream, x, aux, gate, rows, n, dst); break;
+        case 1: launch_kernel(fake_a8_kernel<1>, grid, block, 0, stream, x, aux, gate, rows, n, dst); break;
+        case 2: launch_kernel(fake_a8_kernel<2>, grid, block, 0, stream, x, aux, gate, rows, n, dst); break;
+        default: launch_kernel(fake_a8_kernel<3>, grid, block, 0, stream, x, aux, gate, rows, n, dst); break;
+    }
+    return check_launch("fake_a8");
+}
+
+}  // namespace ndl
+
+using namespace ndl;
+
+extern "C" NDL_API int ndl_hc_mix4(const float *s, int dim, const float *w, int n, float *dst, void *stream) {
+    NDL_REQUIRE(dim >= 1 && n >= 0, "dim %d / n %d", dim, n);
+    if (n == 0) return NDL_OK;
+    NDL_REQUIRE(s && w && dst, "null pointer");
+    return launch_mix4(s, dim, w, n, dst, (cudaStream_t)stream);
+}
+
+extern "C" NDL_API int ndl_hc_combine_diff4x4(const float *s, int dim, const float *mix, const float *x,
+                                              const float *u, const float *post_gate, int n, float *dst,
+                                              void *stream) {
+    NDL_REQUIRE(dim >= 1 && n >= 0, "dim %d / n %d", dim, n);
+    if (n == 0) return NDL_OK;
+    NDL_REQUIRE(s && mix && x && u && post_gate && dst, "null pointer");
+    return launch_combine4(true, s, dim, mix, x, u, post_gate, n, dst, (cudaStream_t)stream);
+}
+
+extern "C" NDL_API int ndl_hc_combine4(const float *s, int dim, const float *w, const float *y, const float *post,
+                                       int n, float *dst, void *stream) {
+    NDL_REQUIRE(dim >= 1 && n >= 0, "dim %d / n %d", dim, n);
+    if (n == 0) return NDL_OK;
+    NDL_REQUIRE(s && w && y && post && dst, "null pointer");
+    return launch_combine4(false, s, dim, w, y, nullptr, post, n, dst, (cudaStream_t)stream);
+}
+
+extern "C" NDL_API int ndl_hc_sinkhorn4x4(const float *logits, int n, float *out, void *stream) {
+    NDL_REQUIRE(n >= 0, "n %d", n);
+    if (n == 0) return NDL_OK;
+    NDL_REQUIRE(logits && out, "null pointer");
+    return launch_sinkhorn4x4(logits, n, out, (cudaStream_t)stream);
+}
+
+extern "C" NDL_API int ndl_taps3(const float *taps, int width, const float *triples, int n, float *dst, void *stream) {
+    NDL_REQUIRE(width >= 1 && n >= 0, "width %d / n %d", width, n);
+    if (n == 0) return NDL_OK;
+    NDL_REQUIRE(taps && triples && dst, "null pointer");
+    return launch_taps3(taps, width, triples, n, dst, (cudaStream_t)stream);
+}
+
+extern "C" NDL_API int ndl_fake_a8_rows(int mode, const float *x, const float *aux, const float *gate, int rows,
+                                        int n, float *dst, void *stream) {
+    NDL_REQUIRE(mode >= 0 && mode <= 3, "mode %d (0..3)", mode);
+    NDL_REQUIRE(rows >= 0 && n >= 1, "rows %d / n %d", rows, n);
+    if (rows == 0) return NDL_OK;
+    NDL_REQUIRE(x && dst && (mode == 0 || aux) && (mode != 3 || gate), "null pointer");
+    return launch_fake_a8(mode, x, aux, gate, rows, n, dst, (cudaStream_t)stream);
+}

@@ -253,6 +253,105 @@ void ndo_swiglu(const float *gate, const float *up, int n, float *dst) {
 }
 
 /* ------------------------------------------------------------------------ */
+/* Needle-3 row ops: hyper-connections, conv taps, fake-A8 norms             */
+/* ------------------------------------------------------------------------ */
+
+/* Scalar.Mix4 (Scalar.cs:255-258): dst = w0*s0 + w1*s1 + w2*s2 + w3*s3. */
+void ndo_mix4(const float *s, int dim, float w0, float w1, float w2, float w3, float *dst) {
+    for (int c = 0; c < dim; c++) dst[c] = w0 * s[c] + w1 * s[dim + c] + w2 * s[2 * dim + c] + w3 * s[3 * dim + c];
+}
+
+/* Scalar.Combine4 (Scalar.cs:250-253): dst = post*y + mix. */
+void ndo_combine4(const float *s, int dim, float w0, float w1, float w2, float w3, const float *y, float post,
+                  float *dst) {
+    for (int c = 0; c < dim; c++)
+        dst[c] = post * y[c] + w0 * s[c] + w1 * s[dim + c] + w2 * s[2 * dim + c] + w3 * s[3 * dim + c];
+}
+
+/* Scalar.CombineDiff4 (Scalar.cs:428-431): dst = post*(x - u) + mix. */
+void ndo_combine_diff4(const float *s, int dim, float w0, float w1, float w2, float w3, const float *x,
+                       const float *u, float post, float *dst) {
+    for (int c = 0; c < dim; c++)
+        dst[c] = post * (x[c] - u[c]) + w0 * s[c] + w1 * s[dim + c] + w2 * s[2 * dim + c] + w3 * s[3 * dim + c];
+}
+
+/* Ops.CombineDiff4x4 (Ops.cs:800-812): lane i of the next stream is
+ * CombineDiff4 with weights mix[4i..4i+3] and gate post_gate[i]. */
+void ndo_combine_diff4x4(const float *s, int dim, const float *mix, const float *x, const float *u,
+                         const float *post_gate, float *dst) {
+    for (int i = 0; i < 4; i++)
+        ndo_combine_diff4(s, dim, mix[i * 4], mix[i * 4 + 1], mix[i * 4 + 2], mix[i * 4 + 3], x, u, post_gate[i],
+                          dst + (size_t)i * dim);
+}
+
+/* Scalar.Taps3 (Scalar.cs:285-288): current[-2w .. w) holds three steps. */
+void ndo_taps3(const float *taps, int width, const float *current, float *dst) {
+    for (int c = 0; c < width; c++)
+        dst[c] = taps[c] * current[c] + taps[width + c] * current[c - width] + taps[2 * width + c] * current[c - 2 * width];
+}
+
+/* Scalar.Sinkhorn4x4 (Scalar.cs:360-379): row-max exp, then 20 rounds of
+ * row and column normalisation (a column of zeros is left alone). */
+void ndo_sinkhorn4x4(const float *logits, float *result) {
+    for (int r = 0; r < 4; r++) {
+        float peak = maxf_cs(maxf_cs(logits[r * 4], logits[r * 4 + 1]), maxf_cs(logits[r * 4 + 2], logits[r * 4 + 3]));
+        for (int c = 0; c < 4; c++) result[r * 4 + c] = expf(logits[r * 4 + c] - peak);
+    }
+    for (int it = 0; it < 20; it++) {
+        for (int r = 0; r < 4; r++) {
+            float sum = result[r * 4] + result[r * 4 + 1] + result[r * 4 + 2] + result[r * 4 + 3];
+            for (int c = 0; c < 4; c++) result[r * 4 + c] /= sum;
+        }
+        for (int c = 0; c < 4; c++) {
+            float sum = result[c] + result[4 + c] + result[8 + c] + result[12 + c];
+            if (sum > 0.0f)
+                for (int r = 0; r < 4; r++) result[r * 4 + c] /= sum;
+        }
+    }
+}
+
+static float fake_round_trip(float *v, int n) {
+    float peak = 0.0f;
+    for (int i = 0; i < n; i++) peak = maxf_cs(peak, fabsf(v[i]));
+    float scale = peak > 0.0f ? peak / 127.0f : 1.0f;
+    float round = 1.0f / scale;
+    for (int i = 0; i < n; i++) v[i] = clamp_q(round_even(v[i] * round)) * scale;
+    return scale;
+}
+
+static float rms_inverse(const float *x, int n) {
+    float sum = 0.0f;
+    for (int i = 0; i < n; i++) sum += x[i] * x[i];
+    return 1.0f / sqrtf(sum / (float)n + 1e-6f);
+}
+
+/* Scalar.RmsFakeA8 (Scalar.cs:381-395). */
+void ndo_rms_fake_a8(const float *x, int n, float *dst) {
+    float inverse = rms_inverse(x, n);
+    for (int i = 0; i < n; i++) dst[i] = x[i] * inverse;
+    fake_round_trip(dst, n);
+}
+
+/* Scalar.CenteredRmsFakeA8 (Scalar.cs:397-411). */
+void ndo_centered_rms_fake_a8(const float *x, const float *scale, int n, float *dst) {
+    float inverse = rms_inverse(x, n);
+    for (int i = 0; i < n; i++) dst[i] = (1.0f + scale[i]) * x[i] * inverse;
+    fake_round_trip(dst, n);
+}
+
+/* Scalar.GateFakeA8 (Scalar.cs:413-426): x *= sigmoid(gate), in place. */
+void ndo_gate_fake_a8(float *x, const float *gate, int n) {
+    for (int i = 0; i < n; i++) x[i] *= ndo_sigmoid(gate[i]);
+    fake_round_trip(x, n);
+}
+
+/* Scalar.PostNormAdd (Scalar.cs:433-439). */
+void ndo_post_norm_add(float *residual, const float *x, const float *scale, float gate, int n) {
+    float inverse = rms_inverse(x, n);
+    for (int i = 0; i < n; i++) residual[i] += gate * ((1.0f + scale[i]) * x[i] * inverse);
+}
+
+/* ------------------------------------------------------------------------ */
 /* Quantized matmul                                                          */
 /* ------------------------------------------------------------------------ */
 

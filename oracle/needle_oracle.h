@@ -58,6 +58,20 @@ typedef struct {
     float byte_scale;
 } ndo_codebook;
 void ndo_codebook_fill(ndo_codebook *book, const float *levels, int count);
+/* Needle-3 row ops (Scalar.cs:250-439, Ops.cs:800-812) */
+void ndo_mix4(const float *s, int dim, float w0, float w1, float w2, float w3, float *dst);
+void ndo_combine4(const float *s, int dim, float w0, float w1, float w2, float w3, const float *y, float post,
+                  float *dst);
+void ndo_combine_diff4(const float *s, int dim, float w0, float w1, float w2, float w3, const float *x,
+                       const float *u, float post, float *dst);
+void ndo_combine_diff4x4(const float *s, int dim, const float *mix, const float *x, const float *u,
+                         const float *post_gate, float *dst);
+void ndo_taps3(const float *taps, int width, const float *current, float *dst);
+void ndo_sinkhorn4x4(const float *logits, float *result);
+void ndo_rms_fake_a8(const float *x, int n, float *dst);
+void ndo_centered_rms_fake_a8(const float *x, const float *scale, int n, float *dst);
+void ndo_gate_fake_a8(float *x, const float *gate, int n);
+void ndo_post_norm_add(float *residual, const float *x, const float *scale, float gate, int n);
 void ndo_gather_row_cq(const uint8_t *indices, const uint16_t *norms, const float *levels, int cols, int bits, int row,
                        float *dst); /* Quant.cs:566-576 */
 

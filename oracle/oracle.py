@@ -46,6 +46,16 @@ _SIGS = {
     "ndo_prepare_cq": (None, [P, I, I, I, P, P, P, I]),
     "ndo_matmul_rows_cq": (None, [P, P, P, I, I, I, P, P, P, I, I, P, I, I, I]),
     "ndo_gather_row_cq": (None, [P, P, P, I, I, I, P]),
+    "ndo_mix4": (None, [P, I, F, F, F, F, P]),
+    "ndo_combine4": (None, [P, I, F, F, F, F, P, F, P]),
+    "ndo_combine_diff4": (None, [P, I, F, F, F, F, P, P, F, P]),
+    "ndo_combine_diff4x4": (None, [P, I, P, P, P, P, P]),
+    "ndo_taps3": (None, [P, I, P, P]),
+    "ndo_sinkhorn4x4": (None, [P, P]),
+    "ndo_rms_fake_a8": (None, [P, I, P]),
+    "ndo_centered_rms_fake_a8": (None, [P, P, I, P]),
+    "ndo_gate_fake_a8": (None, [P, P, I]),
+    "ndo_post_norm_add": (None, [P, P, P, F, I]),
     "ndo_matmul_i8g32": (None, [P, P, I, I, P, P, I, P, P, I]),
     "ndo_attention_head": (None, [P, F, P, P, P, P, I, I, I, I, I, I, I, F, P, P, P]),
     "ndo_merge_partials": (None, [P, I, I, I, I, P]),
@@ -199,6 +209,29 @@ def gather_row_cq(indices, norms, levels, bits, row):
     out = np.empty(cols, np.float32)
     lib().ndo_gather_row_cq(ptr(indices), ptr(norms), ptr(f32(np.resize(np.asarray(levels, np.float32), 16))), cols,
                             bits, row, ptr(out))
+    return out
+
+
+def sinkhorn4x4(logits):
+    """Scalar.Sinkhorn4x4 on one 4x4 logit matrix."""
+    lg = f32(np.asarray(logits, np.float32).reshape(16))
+    out = np.empty(16, np.float32)
+    lib().ndo_sinkhorn4x4(ptr(lg), ptr(out))
+    return out
+
+
+def fake_a8_row(mode, x, aux=None):
+    """RmsFakeA8 (mode 0), CenteredRmsFakeA8 (1, aux = scale), GateFakeA8 (2,
+    aux = gate) on one row."""
+    x = f32(x).copy()
+    out = np.empty_like(x)
+    if mode == 0:
+        lib().ndo_rms_fake_a8(ptr(x), x.size, ptr(out))
+    elif mode == 1:
+        lib().ndo_centered_rms_fake_a8(ptr(x), ptr(f32(aux)), x.size, ptr(out))
+    else:
+        lib().ndo_gate_fake_a8(ptr(x), ptr(f32(aux)), x.size)
+        out = x
     return out
 
 

@@ -1,0 +1,167 @@
+"""Needle-3 row operations on the GPU (hyper-connection mixing, Sinkhorn,
+conv taps, fake-A8 norms): the KernelTable slots 6-13 and 24 with host
+pointers, and the batched device entry points, against the oracle's scalar
+restatements (src/Needle/Scalar.cs:250-439, src/Needle/Ops.cs:800-812).
+
+Bars: bit-exact for everything without exp; GateFakeA8 and Sinkhorn4x4 go
+through CUDA's expf, so GateFakeA8 may differ by one quantization step where
+an ulp moves a value across a rounding boundary, and Sinkhorn4x4 is within
+2e-6 relative (its golden, a zero matrix -> 0.25 everywhere, is exact).
+"""
+import ctypes
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+F = ctypes.c_float
+
+
+def _p(a):
+    return a.ctypes.data
+
+
+def _bits(a):
+    return np.ascontiguousarray(a, np.float32).view(np.uint32)
+
+
+@pytest.fixture(scope="module")
+def lib(pkg, cuda):
+    return pkg.lib()
+
+
+@pytest.fixture(scope="module")
+def olib(oracle):
+    return oracle.lib()
+
+
+def _fill(oracle, seed, n, scale=2.0):
+    return oracle.XorShift64(seed).fill_edges(n, scale)[:n].copy()
+
+
+@pytest.mark.parametrize("dim", [1, 31, 384, 512])
+def test_mix_combine_slots(lib, olib, oracle, dim):
+    s = _fill(oracle, 11 + dim, 4 * dim)
+    x, u, y = _fill(oracle, 12, dim), _fill(oracle, 13, dim), _fill(oracle, 14, dim)
+    w = [0.3, -1.25, 0.875, 2.5]
+    got, want = np.empty(dim, np.float32), np.empty(dim, np.float32)
+    lib.ndl_kt_mix4(_p(s), dim, *w, _p(got))
+    olib.ndo_mix4(_p(s), dim, *w, _p(want))
+    assert np.array_equal(_bits(got), _bits(want))
+    lib.ndl_kt_combine4(_p(s), dim, *w, _p(y), F(0.7), _p(got))
+    olib.ndo_combine4(_p(s), dim, *w, _p(y), 0.7, _p(want))
+    assert np.array_equal(_bits(got), _bits(want))
+    lib.ndl_kt_combine_diff4(_p(s), dim, *w, _p(x), _p(u), F(1.5), _p(got))
+    olib.ndo_combine_diff4(_p(s), dim, *w, _p(x), _p(u), 1.5, _p(want))
+    assert np.array_equal(_bits(got), _bits(want))
+
+
+def test_taps3_slot(lib, olib, oracle):
+    width = 384
+    taps = _fill(oracle, 21, 3 * width)
+    buf = _fill(oracle, 22, 3 * width)  # x_{t-2}, x_{t-1}, x_t; current points at x_t
+    cur = buf.ctypes.data + 2 * width * 4
+    got, want = np.empty(width, np.float32), np.empty(width, np.float32)
+    lib.ndl_kt_taps3(_p(taps), width, cur, _p(got))
+    olib.ndo_taps3(_p(taps), width, ctypes.c_void_p(cur), _p(want))
+    assert np.array_equal(_bits(got), _bits(want))
+
+
+def test_sinkhorn_slot(lib, oracle, golden):
+    out = np.empty(16, np.float32)
+    lib.ndl_kt_sinkhorn4x4(_p(np.zeros(16, np.float32)), _p(out))
+    assert np.array_equal(out, np.float32(golden["fixtures"]["Sinkhorn_zeros_4x4"]))
+    rng = np.random.default_rng(3)
+    for case in range(20):
+        lg = (rng.normal(size=16) * (0.5 + case)).astype(np.float32)
+        lib.ndl_kt_sinkhorn4x4(_p(lg), _p(out))
+        want = oracle.sinkhorn4x4(lg)
+        assert np.allclose(out, want, rtol=2e-6, atol=1e-12), case
+
+
+@pytest.mark.parametrize("n", [1, 5, 384, 512, 2048])
+def test_fake_a8_slots(lib, olib, oracle, n):
+    x = _fill(oracle, 31 + n, n, 3.0)
+    scale = _fill(oracle, 32, n, 0.5)
+    got = np.empty(n, np.float32)
+    lib.ndl_kt_rms_fake_a8(_p(x), n, _p(got))
+    assert np.array_equal(_bits(got), _bits(oracle.fake_a8_row(0, x)))
+    lib.ndl_kt_centered_rms_fake_a8(_p(x), _p(scale), n, _p(got))
+    assert np.array_equal(_bits(got), _bits(oracle.fake_a8_row(1, x, scale)))
+    residual = _fill(oracle, 33, n)
+    want = residual.copy()
+    lib.ndl_kt_post_norm_add(_p(residual), _p(x), _p(scale), F(0.625), n)
+    olib.ndo_post_norm_add(_p(want), _p(x), _p(scale), 0.625, n)
+    assert np.array_equal(_bits(residual), _bits(want))
+    gate = _fill(oracle, 34, n, 4.0)
+    xg = x.copy()
+    lib.ndl_kt_gate_fake_a8(_p(xg), _p(gate), n)
+    want = oracle.fake_a8_row(2, x, gate)
+    step = np.abs(want).max() / 127.0
+    assert np.all(np.abs(xg - want) <= 1.001 * step + 1e-6 * np.abs(want))
+    assert np.mean(xg == want) > 0.99
+
+
+def test_batched_device_entry_points(pkg, olib, oracle):
+    import torch
+
+    from needle_cs_b200 import _native
+
+    dev = torch.device("cuda:0")
+    n, dim = 257, 512
+    rng = np.random.default_rng(9)
+    s = rng.normal(size=(n, 4, dim)).astype(np.float32)
+    w = rng.normal(size=(n, 4)).astype(np.float32)
+    mix = rng.uniform(0, 1, (n, 16)).astype(np.float32)
+    x, u = rng.normal(size=(n, dim)).astype(np.float32), rng.normal(size=(n, dim)).astype(np.float32)
+    gates = rng.uniform(0, 2, (n, 4)).astype(np.float32)
+    t = {k: torch.from_numpy(v).to(dev) for k, v in dict(s=s, w=w, mix=mix, x=x, u=u, g=gates).items()}
+    out = torch.empty((n, dim), device=dev)
+    _native.call("ndl_hc_mix4", t["s"].data_ptr(), dim, t["w"].data_ptr(), n, out.data_ptr(), None)
+    nxt = torch.empty((n, 4, dim), device=dev)
+    _native.call("ndl_hc_combine_diff4x4", t["s"].data_ptr(), dim, t["mix"].data_ptr(), t["x"].data_ptr(),
+                 t["u"].data_ptr(), t["g"].data_ptr(), n, nxt.data_ptr(), None)
+    logits = torch.from_numpy(rng.normal(size=(n, 16)).astype(np.float32) * 3).to(dev)
+    sk = torch.empty((n, 16), device=dev)
+    _native.call("ndl_hc_sinkhorn4x4", logits.data_ptr(), n, sk.data_ptr(), None)
+    torch.cuda.synchronize()
+    got_mix, got_next, got_sk = out.cpu().numpy(), nxt.cpu().numpy(), sk.cpu().numpy()
+    lg = logits.cpu().numpy()
+    want = np.empty(dim, np.float32)
+    want4 = np.empty((4, dim), np.float32)
+    for k in range(n):
+        olib.ndo_mix4(_p(s[k]), dim, *[float(v) for v in w[k]], _p(want))
+        assert np.array_equal(_bits(got_mix[k]), _bits(want)), k
+        olib.ndo_combine_diff4x4(_p(s[k]), dim, _p(mix[k]), _p(x[k]), _p(u[k]), _p(gates[k]), _p(want4))
+        assert np.array_equal(_bits(got_next[k]), _bits(want4)), k
+        assert np.allclose(got_sk[k], oracle.sinkhorn4x4(lg[k]), rtol=2e-6, atol=1e-12), k
+
+    # taps over chained triples, and the fake-A8 rows in every mode
+    width, rows = 384, 64
+    taps = torch.from_numpy(rng.normal(size=3 * width).astype(np.float32)).to(dev)
+    triples = torch.from_numpy(rng.normal(size=(rows, 3, width)).astype(np.float32)).to(dev)
+    tout = torch.empty((rows, width), device=dev)
+    _native.call("ndl_taps3", taps.data_ptr(), width, triples.data_ptr(), rows, tout.data_ptr(), None)
+    xr = torch.from_numpy(rng.normal(size=(rows, width)).astype(np.float32) * 3).to(dev)
+    sc = torch.from_numpy(rng.uniform(-0.5, 0.5, width).astype(np.float32)).to(dev)
+    fa = [torch.empty((rows, width), device=dev) for _ in range(2)]
+    _native.call("ndl_fake_a8_rows", 0, xr.data_ptr(), None, None, rows, width, fa[0].data_ptr(), None)
+    _native.call("ndl_fake_a8_rows", 1, xr.data_ptr(), sc.data_ptr(), None, rows, width, fa[1].data_ptr(), None)
+    res = torch.from_numpy(rng.normal(size=(rows, width)).astype(np.float32)).to(dev)
+    res0 = res.cpu().numpy()
+    rg = torch.from_numpy(rng.uniform(0, 1, rows).astype(np.float32)).to(dev)
+    _native.call("ndl_fake_a8_rows", 3, xr.data_ptr(), sc.data_ptr(), rg.data_ptr(), rows, width, res.data_ptr(), None)
+    torch.cuda.synchronize()
+    tp, tr, xh, sh = taps.cpu().numpy(), triples.cpu().numpy(), xr.cpu().numpy(), sc.cpu().numpy()
+    gh, f0, f1, rh = rg.cpu().numpy(), fa[0].cpu().numpy(), fa[1].cpu().numpy(), res.cpu().numpy()
+    got_t = tout.cpu().numpy()
+    want = np.empty(width, np.float32)
+    for r in range(rows):
+        olib.ndo_taps3(_p(tp), width, ctypes.c_void_p(tr[r].ctypes.data + 2 * width * 4), _p(want))
+        assert np.array_equal(_bits(got_t[r]), _bits(want)), r
+        assert np.array_equal(_bits(f0[r]), _bits(oracle.fake_a8_row(0, xh[r]))), r
+        assert np.array_equal(_bits(f1[r]), _bits(oracle.fake_a8_row(1, xh[r], sh))), r
+        ref = res0[r].copy()
+        olib.ndo_post_norm_add(_p(ref), _p(xh[r]), _p(sh), float(gh[r]), width)
+        assert np.array_equal(_bits(rh[r]), _bits(ref)), r
