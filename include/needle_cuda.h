@@ -266,6 +266,27 @@ NDL_API void ndl_kt_combine4(const float *s, int dim, float w0, float w1, float 
 NDL_API void ndl_kt_taps3(const float *taps, int width, const float *current, float *destination);
 NDL_API void ndl_kt_sinkhorn4x4(const float *logits, float *result);
 
+/* The float helper slots, same conventions:
+ *   Rope               void(float* x, int heads, int headDim, float* cos, float* sin)  slot 14 (x in place)
+ *   ZeroCenteredRms    void(float* x, float* scale, int n, float* destination)  slot 15
+ *   RmsUnit            void(float* x, int n, float* destination)                slot 16
+ *   Softmax            void(float* s, int n)                                    slot 17 (in place)
+ *   Dot                float(float* a, float* b, int n)                         slot 18
+ *   AddScaled          void(float* destination, float* x, float scale, int n)   slot 19
+ *   ScaleAdd           void(float* destination, float scale, float* x, float xScale, int n)  slot 20
+ *   MultiplyAccumulate void(float* destination, float* a, float* b, int n)      slot 21
+ *   FakeA8             float(float* x, int n)                                   slot 23 (x in place)
+ * Bit-exact to the scalar code except Softmax's exp (tolerance). */
+NDL_API void ndl_kt_rope(float *x, int heads, int head_dim, const float *cos_t, const float *sin_t);
+NDL_API void ndl_kt_zero_centered_rms(const float *x, const float *scale, int n, float *destination);
+NDL_API void ndl_kt_rms_unit(const float *x, int n, float *destination);
+NDL_API void ndl_kt_softmax(float *s, int n);
+NDL_API float ndl_kt_dot(const float *a, const float *b, int n);
+NDL_API void ndl_kt_add_scaled(float *destination, const float *x, float scale, int n);
+NDL_API void ndl_kt_scale_add(float *destination, float scale, const float *x, float x_scale, int n);
+NDL_API void ndl_kt_multiply_accumulate(float *destination, const float *a, const float *b, int n);
+NDL_API float ndl_kt_fake_a8(float *x, int n);
+
 /* The same two operations on device memory, stream-ordered: CQ activation
  * prep for `tokens` rows of x [tokens][cols] (values [tokens][cols], scales
  * and offsets [tokens][stride]) and the CQ matmul y[t*ldy + n] for n in

@@ -92,6 +92,15 @@ SIGNATURES = {
     "ndl_kt_combine4": (None, [c_void_p, c_int, c_float, c_float, c_float, c_float, c_void_p, c_float, c_void_p]),
     "ndl_kt_taps3": (None, [c_void_p, c_int, c_void_p, c_void_p]),
     "ndl_kt_sinkhorn4x4": (None, [c_void_p, c_void_p]),
+    "ndl_kt_rope": (None, [c_void_p, c_int, c_int, c_void_p, c_void_p]),
+    "ndl_kt_zero_centered_rms": (None, [c_void_p, c_void_p, c_int, c_void_p]),
+    "ndl_kt_rms_unit": (None, [c_void_p, c_int, c_void_p]),
+    "ndl_kt_softmax": (None, [c_void_p, c_int]),
+    "ndl_kt_dot": (c_float, [c_void_p, c_void_p, c_int]),
+    "ndl_kt_add_scaled": (None, [c_void_p, c_void_p, c_float, c_int]),
+    "ndl_kt_scale_add": (None, [c_void_p, c_float, c_void_p, c_float, c_int]),
+    "ndl_kt_multiply_accumulate": (None, [c_void_p, c_void_p, c_void_p, c_int]),
+    "ndl_kt_fake_a8": (c_float, [c_void_p, c_int]),
     "ndl_hc_mix4": (c_int, [c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p]),
     "ndl_hc_combine4": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_void_p]),
     "ndl_hc_combine_diff4x4": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_void_p]),

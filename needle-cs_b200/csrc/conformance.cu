@@ -35,6 +35,9 @@ int launch_sinkhorn4x4(const float *logits, int n, float *out, cudaStream_t stre
 int launch_taps3(const float *taps, int width, const float *triples, int n, float *dst, cudaStream_t stream);
 int launch_fake_a8(int mode, const float *x, const float *aux, const float *gate, int rows, int n, float *dst,
                    cudaStream_t stream);
+int launch_slot_vec(int mode, float *x, const float *aux, float *dst, float s0, float s1, int n, float *out,
+                    cudaStream_t stream);
+int launch_slot_rope(float *x, int heads, int head_dim, const float *cs, const float *sn, cudaStream_t stream);
 }  // namespace ndl
 
 namespace {
@@ -364,6 +367,106 @@ NDL_API void ndl_kt_sinkhorn4x4(const float *logits, float *result) {
     if (!logits || !result) return (void)set_error(NDL_ERR_INVALID_ARG, "sinkhorn4x4: bad arguments");
     run_floats("sinkhorn4x4", {{logits, 16}}, {{result, 16}},
                [&](auto &i, auto &o) { return launch_sinkhorn4x4(i[0], 1, o[0], nullptr); });
+}
+
+
+// The float helper slots: 14 Rope, 15 ZeroCenteredRms, 16 RmsUnit, 17 Softmax,
+// 18 Dot, 19 AddScaled, 20 ScaleAdd, 21 MultiplyAccumulate, 23 FakeA8.
+NDL_API void ndl_kt_rope(float *x, int heads, int head_dim, const float *cos_t, const float *sin_t) {
+    std::lock_guard<std::mutex> lock(g_mu);
+    if (!x || !cos_t || !sin_t || heads < 0 || head_dim < 2 || head_dim % 2)
+        return (void)set_error(NDL_ERR_INVALID_ARG, "rope: bad arguments");
+    const size_t n = (size_t)heads * head_dim, half = head_dim / 2;
+    run_floats("rope", {{x, n}, {cos_t, half}, {sin_t, half}}, {{x, n}}, [&](auto &i, auto &o) -> int {
+        if (cudaMemcpy(o[0], i[0], n * 4, cudaMemcpyDeviceToDevice) != cudaSuccess) return (int)NDL_ERR_CUDA;
+        return launch_slot_rope(o[0], heads, head_dim, i[1], i[2], nullptr);
+    });
+}
+
+NDL_API void ndl_kt_zero_centered_rms(const float *x, const float *scale, int n, float *destination) {
+    std::lock_guard<std::mutex> lock(g_mu);
+    if (!x || !scale || !destination || n < 1) return (void)set_error(NDL_ERR_INVALID_ARG, "zero_centered_rms: bad arguments");
+    run_floats("zero_centered_rms", {{x, (size_t)n}, {scale, (size_t)n}}, {{destination, (size_t)n}},
+               [&](auto &i, auto &o) { return launch_slot_vec(1, i[0], i[1], o[0], 0, 0, n, nullptr, nullptr); });
+}
+
+NDL_API void ndl_kt_rms_unit(const float *x, int n, float *destination) {
+    std::lock_guard<std::mutex> lock(g_mu);
+    if (!x || !destination || n < 1) return (void)set_error(NDL_ERR_INVALID_ARG, "rms_unit: bad arguments");
+    run_floats("rms_unit", {{x, (size_t)n}}, {{destination, (size_t)n}},
+               [&](auto &i, auto &o) { return launch_slot_vec(0, i[0], nullptr, o[0], 0, 0, n, nullptr, nullptr); });
+}
+
+NDL_API void ndl_kt_softmax(float *s, int n) {
+    std::lock_guard<std::mutex> lock(g_mu);
+    if (!s || n < 1) return (void)set_error(NDL_ERR_INVALID_ARG, "softmax: bad arguments");
+    run_floats("softmax", {{s, (size_t)n}}, {{s, (size_t)n}}, [&](auto &i, auto &o) -> int {
+        if (cudaMemcpy(o[0], i[0], (size_t)n * 4, cudaMemcpyDeviceToDevice) != cudaSuccess) return (int)NDL_ERR_CUDA;
+        return launch_slot_vec(6, o[0], nullptr, nullptr, 0, 0, n, nullptr, nullptr);
+    });
+}
+
+NDL_API float ndl_kt_dot(const float *a, const float *b, int n) {
+    std::lock_guard<std::mutex> lock(g_mu);
+    if (!a || !b || n < 0) {
+        set_error(NDL_ERR_INVALID_ARG, "dot: bad arguments");
+        return NAN;
+    }
+    if (n == 0) return 0.0f;
+    float r = NAN;
+    if (!run_floats("dot", {{a, (size_t)n}, {b, (size_t)n}}, {{&r, 1}}, [&](auto &i, auto &o) {
+            return launch_slot_vec(5, i[0], i[1], nullptr, 0, 0, n, o[0], nullptr);
+        }))
+        return NAN;
+    return r;
+}
+
+NDL_API void ndl_kt_add_scaled(float *destination, const float *x, float scale, int n) {
+    std::lock_guard<std::mutex> lock(g_mu);
+    if (!destination || !x || n < 1) return (void)set_error(NDL_ERR_INVALID_ARG, "add_scaled: bad arguments");
+    run_floats("add_scaled", {{x, (size_t)n}, {destination, (size_t)n}}, {{destination, (size_t)n}},
+               [&](auto &i, auto &o) -> int {
+                   if (cudaMemcpy(o[0], i[1], (size_t)n * 4, cudaMemcpyDeviceToDevice) != cudaSuccess)
+                       return (int)NDL_ERR_CUDA;
+                   return launch_slot_vec(2, i[0], nullptr, o[0], scale, 0, n, nullptr, nullptr);
+               });
+}
+
+NDL_API void ndl_kt_scale_add(float *destination, float scale, const float *x, float x_scale, int n) {
+    std::lock_guard<std::mutex> lock(g_mu);
+    if (!destination || !x || n < 1) return (void)set_error(NDL_ERR_INVALID_ARG, "scale_add: bad arguments");
+    run_floats("scale_add", {{x, (size_t)n}, {destination, (size_t)n}}, {{destination, (size_t)n}},
+               [&](auto &i, auto &o) -> int {
+                   if (cudaMemcpy(o[0], i[1], (size_t)n * 4, cudaMemcpyDeviceToDevice) != cudaSuccess)
+                       return (int)NDL_ERR_CUDA;
+                   return launch_slot_vec(3, i[0], nullptr, o[0], scale, x_scale, n, nullptr, nullptr);
+               });
+}
+
+NDL_API void ndl_kt_multiply_accumulate(float *destination, const float *a, const float *b, int n) {
+    std::lock_guard<std::mutex> lock(g_mu);
+    if (!destination || !a || !b || n < 1) return (void)set_error(NDL_ERR_INVALID_ARG, "multiply_accumulate: bad arguments");
+    run_floats("multiply_accumulate", {{a, (size_t)n}, {b, (size_t)n}, {destination, (size_t)n}},
+               {{destination, (size_t)n}}, [&](auto &i, auto &o) -> int {
+                   if (cudaMemcpy(o[0], i[2], (size_t)n * 4, cudaMemcpyDeviceToDevice) != cudaSuccess)
+                       return (int)NDL_ERR_CUDA;
+                   return launch_slot_vec(4, i[0], i[1], o[0], 0, 0, n, nullptr, nullptr);
+               });
+}
+
+NDL_API float ndl_kt_fake_a8(float *x, int n) {
+    std::lock_guard<std::mutex> lock(g_mu);
+    if (!x || n < 1) {
+        set_error(NDL_ERR_INVALID_ARG, "fake_a8: bad arguments");
+        return NAN;
+    }
+    float scale = NAN;
+    if (!run_floats("fake_a8", {{x, (size_t)n}}, {{x, (size_t)n}, {&scale, 1}}, [&](auto &i, auto &o) -> int {
+            if (cudaMemcpy(o[0], i[0], (size_t)n * 4, cudaMemcpyDeviceToDevice) != cudaSuccess) return (int)NDL_ERR_CUDA;
+            return launch_slot_vec(7, o[0], nullptr, nullptr, 0, 0, n, o[1], nullptr);
+        }))
+        return NAN;
+    return scale;
 }
 
 }  // extern "C"

@@ -157,6 +157,99 @@ __global__ void __launch_bounds__(256) fake_a8_kernel(const float *__restrict__ 
     }
 }
 
+// The plain float helper slots (Scalar.cs:206-248, Ops.cs:209-255, Quant.cs:69-80)
+// on one warp: sums run on lane 0 in ascending order, so the results equal the
+// scalar code (Softmax's exp aside).  MODE 0 RmsUnit, 1 ZeroCenteredRms
+// (aux = scale), 2 AddScaled, 3 ScaleAdd, 4 MultiplyAccumulate (aux = b),
+// 5 Dot (aux = b, result in out[0]), 6 Softmax (x in place), 7 FakeA8 (x in
+// place, scale in out[0]).  dst is the slot's destination.
+template <int MODE>
+__global__ void __launch_bounds__(32) slot_vec_kernel(float *__restrict__ x, const float *__restrict__ aux,
+                                                      float *__restrict__ dst, float s0, float s1, int n,
+                                                      float *__restrict__ out) {
+    const int lane = threadIdx.x;
+    if (MODE == 0 || MODE == 1) {
+        float sum = 0.0f;
+        if (lane == 0)
+            for (int i = 0; i < n; i++) sum = __fadd_rn(sum, __fmul_rn(x[i], x[i]));
+        sum = __shfl_sync(0xffffffffu, sum, 0);
+        const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, (float)n), 1e-6f)));
+        for (int i = lane; i < n; i += 32)
+            dst[i] = MODE == 0 ? __fmul_rn(x[i], inv) : __fmul_rn(__fmul_rn(__fadd_rn(1.0f, aux[i]), x[i]), inv);
+    } else if (MODE == 2) {
+        for (int i = lane; i < n; i += 32) dst[i] = __fadd_rn(dst[i], __fmul_rn(s0, x[i]));
+    } else if (MODE == 3) {
+        for (int i = lane; i < n; i += 32) dst[i] = __fadd_rn(__fmul_rn(s0, dst[i]), __fmul_rn(s1, x[i]));
+    } else if (MODE == 4) {
+        for (int i = lane; i < n; i += 32) dst[i] = __fadd_rn(dst[i], __fmul_rn(x[i], aux[i]));
+    } else if (MODE == 5) {
+        if (lane == 0) {
+            float sum = 0.0f;
+            for (int i = 0; i < n; i++) sum = __fadd_rn(sum, __fmul_rn(x[i], aux[i]));
+            out[0] = sum;
+        }
+    } else if (MODE == 6) {
+        float peak = -INFINITY;
+        for (int i = lane; i < n; i += 32) peak = fmaxf(peak, x[i]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) peak = fmaxf(peak, __shfl_xor_sync(0xffffffffu, peak, o));
+        for (int i = lane; i < n; i += 32) x[i] = expf(__fsub_rn(x[i], peak));
+        __syncwarp();
+        float total = 0.0f;
+        if (lane == 0)
+            for (int i = 0; i < n; i++) total = __fadd_rn(total, x[i]);
+        total = __shfl_sync(0xffffffffu, total, 0);
+        for (int i = lane; i < n; i += 32) x[i] = __fdiv_rn(x[i], total);
+    } else {  // FakeA8: AbsMax, then RoundTrip with the reference's RoundEven
+        float peak = 0.0f;
+        for (int i = lane; i < n; i += 32) peak = fmaxf(peak, fabsf(x[i]));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) peak = fmaxf(peak, __shfl_xor_sync(0xffffffffu, peak, o));
+        const float scale = peak > 0.0f ? __fdiv_rn(peak, 127.0f) : 1.0f;
+        const float inverse = __fdiv_rn(1.0f, scale);
+        for (int i = lane; i < n; i += 32) {
+            const float r = __fsub_rn(__fadd_rn(__fmul_rn(x[i], inverse), 12582912.0f), 12582912.0f);
+            x[i] = __fmul_rn(fminf(fmaxf(r, -128.0f), 127.0f), scale);
+        }
+        if (lane == 0) out[0] = scale;
+    }
+}
+
+// Scalar.Rope (Scalar.cs:233-248): half-split rotation of each head, in place.
+__global__ void __launch_bounds__(256) slot_rope_kernel(float *__restrict__ x, int heads, int head_dim,
+                                                        const float *__restrict__ cs, const float *__restrict__ sn) {
+    const int half = head_dim / 2;
+    const int k = blockIdx.x * blockDim.x + threadIdx.x;
+    if (k >= heads * half) return;
+    const int h = k / half, i = k - h * half;
+    float *lo = x + (size_t)h * head_dim, *hi = lo + half;
+    const float a = lo[i], b = hi[i];
+    lo[i] = __fsub_rn(__fmul_rn(a, cs[i]), __fmul_rn(b, sn[i]));
+    hi[i] = __fadd_rn(__fmul_rn(b, cs[i]), __fmul_rn(a, sn[i]));
+}
+
+int launch_slot_vec(int mode, float *x, const float *aux, float *dst, float s0, float s1, int n, float *out,
+                    cudaStream_t stream) {
+    switch (mode) {
+        case 0: slot_vec_kernel<0><<<1, 32, 0, stream>>>(x, aux, dst, s0, s1, n, out); break;
+        case 1: slot_vec_kernel<1><<<1, 32, 0, stream>>>(x, aux, dst, s0, s1, n, out); break;
+        case 2: slot_vec_kernel<2><<<1, 32, 0, stream>>>(x, aux, dst, s0, s1, n, out); break;
+        case 3: slot_vec_kernel<3><<<1, 32, 0, stream>>>(x, aux, dst, s0, s1, n, out); break;
+        case 4: slot_vec_kernel<4><<<1, 32, 0, stream>>>(x, aux, dst, s0, s1, n, out); break;
+        case 5: slot_vec_kernel<5><<<1, 32, 0, stream>>>(x, aux, dst, s0, s1, n, out); break;
+        case 6: slot_vec_kernel<6><<<1, 32, 0, stream>>>(x, aux, dst, s0, s1, n, out); break;
+        default: slot_vec_kernel<7><<<1, 32, 0, stream>>>(x, aux, dst, s0, s1, n, out); break;
+    }
+    return check_launch("slot_vec");
+}
+
+int launch_slot_rope(float *x, int heads, int head_dim, const float *cs, const float *sn, cudaStream_t stream) {
+    const int k = heads * (head_dim / 2);
+    if (k == 0) return NDL_OK;
+    slot_rope_kernel<<<(k + 255) / 256, 256, 0, stream>>>(x, heads, head_dim, cs, sn);
+    return check_launch("slot_rope");
+}
+
 static unsigned blocks_for(long long threads, int per_block) {
     return (unsigned)((threads + per_block - 1) / per_block);
 }

@@ -165,3 +165,66 @@ def test_batched_device_entry_points(pkg, olib, oracle):
         ref = res0[r].copy()
         olib.ndo_post_norm_add(_p(ref), _p(xh[r]), _p(sh), float(gh[r]), width)
         assert np.array_equal(_bits(rh[r]), _bits(ref)), r
+
+
+def test_float_helper_slots(lib, olib, oracle, golden):
+    """Slots 14-21 and 23 against the oracle and the reference's goldens."""
+    fx = golden["fixtures"]
+    rng = np.random.default_rng(21)
+    n = 777
+    x = (rng.normal(size=n) * 2).astype(np.float32)
+    b = (rng.normal(size=n)).astype(np.float32)
+    got = np.empty(n, np.float32)
+    lib.ndl_kt_rms_unit(_p(x), n, _p(got))
+    inv = np.float32(olib.ndo_inverse_rms(_p(x), n))
+    assert np.array_equal(_bits(got), _bits(x * inv))
+    scale = (rng.uniform(-0.5, 0.5, n)).astype(np.float32)
+    want = np.empty(n, np.float32)
+    lib.ndl_kt_zero_centered_rms(_p(x), _p(scale), n, _p(got))
+    olib.ndo_zero_centered_rms(_p(x), _p(scale), n, _p(want))
+    assert np.array_equal(_bits(got), _bits(want))
+    # Dot: sequential fp32 sum, and its golden
+    d = lib.ndl_kt_dot(_p(x), _p(b), n)
+    acc = np.float32(0)
+    for i in range(n):
+        acc = np.float32(acc + np.float32(x[i] * b[i]))
+    assert np.float32(d).view(np.uint32) == acc.view(np.uint32)
+    a8 = np.arange(1, 9, dtype=np.float32)
+    assert lib.ndl_kt_dot(_p(a8), _p(a8[::-1].copy()), 8) == fx["Dot_1to8_8to1"]
+    # AddScaled, ScaleAdd, MultiplyAccumulate: one rounding per operation
+    dst = (rng.normal(size=n)).astype(np.float32)
+    out = dst.copy()
+    lib.ndl_kt_add_scaled(_p(out), _p(x), F(0.75), n)
+    assert np.array_equal(_bits(out), _bits(dst + np.float32(0.75) * x))
+    out = dst.copy()
+    lib.ndl_kt_scale_add(_p(out), F(-1.5), _p(x), F(0.25), n)
+    assert np.array_equal(_bits(out), _bits(np.float32(-1.5) * dst + np.float32(0.25) * x))
+    out = dst.copy()
+    lib.ndl_kt_multiply_accumulate(_p(out), _p(x), _p(b), n)
+    assert np.array_equal(_bits(out), _bits(dst + x * b))
+    # Softmax (exp: tolerance) and its goldens
+    for inp, key in (([0, 0, 0], "Softmax_0_0_0"), ([1, 2, 3], "Softmax_1_2_3")):
+        v = np.float32(inp)
+        lib.ndl_kt_softmax(_p(v), 3)
+        assert np.allclose(v, np.float32(fx[key]), rtol=2e-7, atol=1e-7)
+    v, w = x.copy(), x.copy()
+    lib.ndl_kt_softmax(_p(v), n)
+    olib.ndo_softmax(_p(w), n)
+    assert np.allclose(v, w, rtol=1e-6, atol=1e-12)
+    # FakeA8: bit-exact, half-to-even ties at a unit scale
+    v, w = x.copy(), x.copy()
+    sc = lib.ndl_kt_fake_a8(_p(v), n)
+    sw = olib.ndo_fake_a8(_p(w), n)
+    assert np.float32(sc) == np.float32(sw) and np.array_equal(_bits(v), _bits(w))
+    ties = np.float32([127.0, 0.5, 2.5, -0.5])
+    lib.ndl_kt_fake_a8(_p(ties), 4)
+    assert ties[1] == fx["FakeA8_tie_0_5"] and ties[2] == fx["FakeA8_tie_2_5"] and ties[3] == 0.0
+    # Rope over 6 heads of 64 at position 37
+    heads, hd = 6, 64
+    cs, sn = oracle.rope_tables(10000.0, hd, 64)
+    cs, sn = np.ascontiguousarray(cs.reshape(64, -1)[37]), np.ascontiguousarray(sn.reshape(64, -1)[37])
+    q = (rng.normal(size=heads * hd)).astype(np.float32)
+    r1, r2 = q.copy(), q.copy()
+    lib.ndl_kt_rope(_p(r1), heads, hd, _p(cs), _p(sn))
+    olib.ndo_rope(_p(r2), heads, hd, _p(cs), _p(sn))
+    assert np.array_equal(_bits(r1), _bits(r2))
