@@ -287,6 +287,53 @@ NDL_API void ndl_kt_scale_add(float *destination, float scale, const float *x, f
 NDL_API void ndl_kt_multiply_accumulate(float *destination, const float *a, const float *b, int n);
 NDL_API float ndl_kt_fake_a8(float *x, int n);
 
+/* AttentionTile  void(AttentionTile* tile)  slot 3 and MergePartials
+ * void(float* partials, int count, int heads, float* output)  slot 4 (the
+ * reference's tile: 48-dim int8 keys, 64-dim values, up to 6 heads,
+ * src/Needle/Blocks.cs:11-27,65-84,750-817).  With peaks and sums set the
+ * tile's outputs are unnormalized and each head's peak and exp sum are
+ * stored (the split-position mode); MergePartials combines `count` slots of
+ * 6*64 + 16 floats.  fp32 throughout; tolerance-equal to the scalar code. */
+typedef struct {
+    const int8_t *queries;      /* [heads][48] */
+    const float *query_scales;  /* [heads] */
+    int heads;
+    const int8_t *keys;         /* row p at keys + p * key_stride */
+    const float *key_scales;    /* [p * scale_stride] */
+    const int8_t *values;
+    const float *value_scales;
+    int key_stride, value_stride, scale_stride, first, count;
+    float *scores;              /* scratch, >= count floats */
+    float *output;              /* [heads][64] */
+    float *probabilities;       /* nullable: head h at + h * probability_stride + first */
+    int probability_stride;
+    float *peaks;               /* nullable (with sums): [heads] */
+    float *sums;
+} ndl_kt_tile;
+NDL_API void ndl_kt_attention_tile(const ndl_kt_tile *tile);
+NDL_API void ndl_kt_merge_partials(const float *partials, int count, int heads, float *output);
+
+/* HadamardMlpApply  void(MlpBatch* b, float* residual, float* scratch)  slot 5
+ * (HadamardMlp.Apply, src/Needle/Blocks.cs:1067-1093): the Kronecker-factored
+ * MLP on one token's residual row, updated in place; MlpWeights and MlpBatch
+ * in the reference's sequential layouts (src/Needle/Audio.cs:5-27,
+ * src/Needle/Blocks.cs:992-1004).  Inner sums in the scalar order; the
+ * condition softmax and the SiLU go through expf (tolerance). */
+typedef struct {
+    const float *d1, *d2, *b2, *d3, *d4;
+    const float *w1a, *w1b, *w2a, *w2b, *w3a, *w3b;
+    const float *cond_v, *cond_u;
+} ndl_kt_mlp_weights;
+typedef struct {
+    const ndl_kt_mlp_weights *weights;
+    const float *pre_norm;
+    const int32_t *perm_a, *perm_b;
+    float *residual;  /* unused by the slot (the row comes as an argument) */
+    int dim, rows, cols;
+    float scale;
+} ndl_kt_mlp_batch;
+NDL_API void ndl_kt_hadamard_mlp(const ndl_kt_mlp_batch *b, float *residual, float *scratch);
+
 /* The same two operations on device memory, stream-ordered: CQ activation
  * prep for `tokens` rows of x [tokens][cols] (values [tokens][cols], scales
  * and offsets [tokens][stride]) and the CQ matmul y[t*ldy + n] for n in

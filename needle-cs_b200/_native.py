@@ -101,6 +101,9 @@ SIGNATURES = {
     "ndl_kt_scale_add": (None, [c_void_p, c_float, c_void_p, c_float, c_int]),
     "ndl_kt_multiply_accumulate": (None, [c_void_p, c_void_p, c_void_p, c_int]),
     "ndl_kt_fake_a8": (c_float, [c_void_p, c_int]),
+    "ndl_kt_attention_tile": (None, [c_void_p]),
+    "ndl_kt_merge_partials": (None, [c_void_p, c_int, c_int, c_void_p]),
+    "ndl_kt_hadamard_mlp": (None, [c_void_p, c_void_p, c_void_p]),
     "ndl_hc_mix4": (c_int, [c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p]),
     "ndl_hc_combine4": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_void_p]),
     "ndl_hc_combine_diff4x4": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_void_p]),

@@ -38,6 +38,31 @@ int launch_fake_a8(int mode, const float *x, const float *aux, const float *gate
 int launch_slot_vec(int mode, float *x, const float *aux, float *dst, float s0, float s1, int n, float *out,
                     cudaStream_t stream);
 int launch_slot_rope(float *x, int heads, int head_dim, const float *cs, const float *sn, cudaStream_t stream);
+struct KtTileArgs {
+    const int8_t *q;
+    const float *qs;
+    int heads;
+    const int8_t *keys;
+    const float *ks;
+    const int8_t *values;
+    const float *vs;
+    int key_stride, value_stride, scale_stride, count;
+    float *scores;
+    float *output;
+    float *probs;
+    float *peaks, *sums;
+};
+int launch_slot_attention_tile(const KtTileArgs &a, cudaStream_t stream);
+int launch_slot_merge_partials(const float *partials, int count, int heads, float *out, cudaStream_t stream);
+struct KtMlpArgs {
+    const float *w[13];
+    const float *pre_norm;
+    const int32_t *perm_a, *perm_b;
+    int dim, rows, cols;
+    float scale;
+    float *residual;
+};
+int launch_slot_hadamard_mlp(const KtMlpArgs &a, cudaStream_t stream);
 }  // namespace ndl
 
 namespace {
@@ -467,6 +492,134 @@ NDL_API float ndl_kt_fake_a8(float *x, int n) {
         }))
         return NAN;
     return scale;
+}
+
+
+// void AttentionTile(AttentionTile* tile)  slot 3: 48-dim keys, 64-dim values, up
+// to 6 heads over one span (Attention.Run, src/Needle/Blocks.cs:65-84).
+NDL_API void ndl_kt_attention_tile(const ndl_kt_tile *t) {
+    std::lock_guard<std::mutex> lock(g_mu);
+    if (!t || t->heads < 1 || t->heads > 6 || t->count < 1 || t->first < 0 || !t->queries || !t->query_scales ||
+        !t->keys || !t->key_scales || !t->values || !t->value_scales || !t->output || !t->scores ||
+        t->key_stride < 48 || t->value_stride < 64 || t->scale_stride < 1 || (!t->peaks) != (!t->sums) ||
+        (t->probabilities && t->probability_stride < t->first + t->count)) {
+        set_error(NDL_ERR_INVALID_ARG, "attention_tile: bad arguments");
+        return;
+    }
+    const int H = t->heads, n = t->count;
+    const size_t kb = (size_t)(n - 1) * t->key_stride + 48, vb = (size_t)(n - 1) * t->value_stride + 64;
+    const size_t sf = (size_t)(n - 1) * t->scale_stride + 1;
+    const size_t sizes[] = {align16((size_t)H * 48), align16((size_t)H * 4), align16(kb), align16(vb), align16(sf * 4),
+                            align16(sf * 4), align16((size_t)H * n * 4), align16((size_t)H * 64 * 4),
+                            align16((size_t)H * n * 4), align16((size_t)H * 4), align16((size_t)H * 4)};
+    size_t total = 0;
+    for (size_t z : sizes) total += z;
+    void *buf = nullptr;
+    if (scratch(total, &buf) != NDL_OK) return;
+    char *p = static_cast<char *>(buf);
+    char *ptrs[11];
+    for (int i = 0; i < 11; i++) ptrs[i] = p, p += sizes[i];
+    KtTileArgs a{reinterpret_cast<int8_t *>(ptrs[0]), reinterpret_cast<float *>(ptrs[1]), H,
+                 reinterpret_cast<int8_t *>(ptrs[2]), reinterpret_cast<float *>(ptrs[4]),
+                 reinterpret_cast<int8_t *>(ptrs[3]), reinterpret_cast<float *>(ptrs[5]), t->key_stride,
+                 t->value_stride, t->scale_stride, n, reinterpret_cast<float *>(ptrs[6]),
+                 reinterpret_cast<float *>(ptrs[7]), t->probabilities ? reinterpret_cast<float *>(ptrs[8]) : nullptr,
+                 t->peaks ? reinterpret_cast<float *>(ptrs[9]) : nullptr,
+                 t->sums ? reinterpret_cast<float *>(ptrs[10]) : nullptr};
+    const size_t first = (size_t)t->first;
+    bool ok = cudaMemcpy(ptrs[0], t->queries, (size_t)H * 48, cudaMemcpyHostToDevice) == cudaSuccess &&
+              cudaMemcpy(ptrs[1], t->query_scales, (size_t)H * 4, cudaMemcpyHostToDevice) == cudaSuccess &&
+              cudaMemcpy(ptrs[2], t->keys + first * t->key_stride, kb, cudaMemcpyHostToDevice) == cudaSuccess &&
+              cudaMemcpy(ptrs[3], t->values + first * t->value_stride, vb, cudaMemcpyHostToDevice) == cudaSuccess &&
+              cudaMemcpy(ptrs[4], t->key_scales + first * t->scale_stride, sf * 4, cudaMemcpyHostToDevice) == cudaSuccess &&
+              cudaMemcpy(ptrs[5], t->value_scales + first * t->scale_stride, sf * 4, cudaMemcpyHostToDevice) ==
+                  cudaSuccess &&
+              launch_slot_attention_tile(a, nullptr) == NDL_OK &&
+              cudaMemcpy(t->output, ptrs[7], (size_t)H * 64 * 4, cudaMemcpyDeviceToHost) == cudaSuccess &&
+              cudaMemcpy(t->scores, ptrs[6] + (size_t)(H - 1) * n * 4, (size_t)n * 4, cudaMemcpyDeviceToHost) ==
+                  cudaSuccess;  // the reference's scratch ends with the last head's scores
+    if (ok && t->probabilities)
+        ok = cudaMemcpy2D(t->probabilities + first, (size_t)t->probability_stride * 4, ptrs[8], (size_t)n * 4,
+                          (size_t)n * 4, H, cudaMemcpyDeviceToHost) == cudaSuccess;
+    if (ok && t->peaks)
+        ok = cudaMemcpy(t->peaks, ptrs[9], (size_t)H * 4, cudaMemcpyDeviceToHost) == cudaSuccess &&
+             cudaMemcpy(t->sums, ptrs[10], (size_t)H * 4, cudaMemcpyDeviceToHost) == cudaSuccess;
+    if (!ok) {
+        cudaGetLastError();
+        set_error(NDL_ERR_CUDA, "attention_tile failed");
+    }
+}
+
+// void MergePartials(float* partials, int count, int heads, float* output)  slot 4
+NDL_API void ndl_kt_merge_partials(const float *partials, int count, int heads, float *output) {
+    std::lock_guard<std::mutex> lock(g_mu);
+    if (!partials || !output || count < 1 || heads < 1 || heads > 6)
+        return (void)set_error(NDL_ERR_INVALID_ARG, "merge_partials: bad arguments");
+    run_floats("merge_partials", {{partials, (size_t)count * (6 * 64 + 16)}}, {{output, (size_t)heads * 64}},
+               [&](auto &i, auto &o) { return launch_slot_merge_partials(i[0], count, heads, o[0], nullptr); });
+}
+
+// void HadamardMlpApply(MlpBatch* b, float* residual, float* scratch)  slot 5
+// (HadamardMlp.Apply, src/Needle/Blocks.cs:1067-1093): the residual row is
+// updated in place; the reference's scratch argument is not used.
+NDL_API void ndl_kt_hadamard_mlp(const ndl_kt_mlp_batch *b, float *residual, float *work) {
+    (void)work;
+    std::lock_guard<std::mutex> lock(g_mu);
+    if (!b || !b->weights || !residual || !b->pre_norm || !b->perm_a || !b->perm_b || b->dim < 1 || b->rows < 1 ||
+        b->cols < 1 || b->cols > 1024) {
+        set_error(NDL_ERR_INVALID_ARG, "hadamard_mlp: bad arguments");
+        return;
+    }
+    const int dim = b->dim, rows = b->rows, cols = b->cols, width = rows * cols, in_rows = (dim + cols - 1) / cols;
+    if (in_rows > rows) return (void)set_error(NDL_ERR_INVALID_ARG, "hadamard_mlp: dim %d beyond %d x %d", dim, rows, cols);
+    for (int n = 0; n < width; n++)
+        if (b->perm_a[n] < 0 || b->perm_a[n] >= width || b->perm_b[n] < 0 || b->perm_b[n] >= width)
+            return (void)set_error(NDL_ERR_INVALID_ARG, "hadamard_mlp: permutation entry out of range");
+    const ndl_kt_mlp_weights &w = *b->weights;
+    const float *src[13] = {w.d1, w.d2, w.b2, w.d3, w.d4, w.w1a, w.w1b, w.w2a, w.w2b, w.w3a, w.w3b, w.cond_v, w.cond_u};
+    const size_t cnt[13] = {(size_t)dim, (size_t)width, (size_t)width, (size_t)width, (size_t)dim,
+                            (size_t)in_rows * rows, (size_t)cols * cols, (size_t)rows * rows, (size_t)cols * cols,
+                            (size_t)rows * rows, (size_t)cols * cols, (size_t)dim * 8, (size_t)8 * width};
+    size_t total = align16((size_t)dim * 4) * 2 + align16((size_t)width * 4) * 2;
+    for (int k = 0; k < 13; k++) {
+        if (!src[k]) return (void)set_error(NDL_ERR_INVALID_ARG, "hadamard_mlp: null weight array %d", k);
+        total += align16(cnt[k] * 4);
+    }
+    void *buf = nullptr;
+    if (scratch(total, &buf) != NDL_OK) return;
+    char *p = static_cast<char *>(buf);
+    KtMlpArgs a{};
+    bool ok = true;
+    for (int k = 0; k < 13; k++) {
+        a.w[k] = reinterpret_cast<const float *>(p);
+        ok = ok && cudaMemcpy(p, src[k], cnt[k] * 4, cudaMemcpyHostToDevice) == cudaSuccess;
+        p += align16(cnt[k] * 4);
+    }
+    float *d_pre = reinterpret_cast<float *>(p);
+    p += align16((size_t)dim * 4);
+    float *d_res = reinterpret_cast<float *>(p);
+    p += align16((size_t)dim * 4);
+    int32_t *d_pa = reinterpret_cast<int32_t *>(p);
+    p += align16((size_t)width * 4);
+    int32_t *d_pb = reinterpret_cast<int32_t *>(p);
+    ok = ok && cudaMemcpy(d_pre, b->pre_norm, (size_t)dim * 4, cudaMemcpyHostToDevice) == cudaSuccess &&
+         cudaMemcpy(d_res, residual, (size_t)dim * 4, cudaMemcpyHostToDevice) == cudaSuccess &&
+         cudaMemcpy(d_pa, b->perm_a, (size_t)width * 4, cudaMemcpyHostToDevice) == cudaSuccess &&
+         cudaMemcpy(d_pb, b->perm_b, (size_t)width * 4, cudaMemcpyHostToDevice) == cudaSuccess;
+    a.pre_norm = d_pre;
+    a.perm_a = d_pa;
+    a.perm_b = d_pb;
+    a.dim = dim;
+    a.rows = rows;
+    a.cols = cols;
+    a.scale = b->scale;
+    a.residual = d_res;
+    ok = ok && launch_slot_hadamard_mlp(a, nullptr) == NDL_OK &&
+         cudaMemcpy(residual, d_res, (size_t)dim * 4, cudaMemcpyDeviceToHost) == cudaSuccess;
+    if (!ok) {
+        cudaGetLastError();
+        set_error(NDL_ERR_CUDA, "hadamard_mlp failed");
+    }
 }
 
 }  // extern "C"

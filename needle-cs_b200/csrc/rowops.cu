@@ -250,6 +250,211 @@ int launch_slot_rope(float *x, int heads, int head_dim, const float *cs, const f
     return check_launch("slot_rope");
 }
 
+// Attention.Run / Scalar.AttentionTile (src/Needle/Blocks.cs:65-84,
+// src/Needle/Scalar.cs:290-321) on the reference's tile: up to 6 query heads
+// sharing one key / value span, keys of 48 int8, values of 64.  Warp per
+// head.  Without peaks the outputs are normalized (Softmax, then the
+// weighted value sum); with peaks (the split-position mode of the
+// reference's vector path, Blocks.cs:188-199) the outputs stay unnormalized
+// and the head's peak and exp sum are stored for MergePartials.  Positions
+// are summed in ascending order.
+struct KtTileArgs {
+    const int8_t *q;
+    const float *qs;
+    int heads;
+    const int8_t *keys;  // row 0 = the tile's first position
+    const float *ks;
+    const int8_t *values;
+    const float *vs;
+    int key_stride, value_stride, scale_stride, count;
+    float *scores;  // [heads][count]
+    float *output;  // [heads][64]
+    float *probs;   // [heads][count] or null
+    float *peaks, *sums;  // [heads] or null
+};
+
+__global__ void __launch_bounds__(192) slot_attention_tile_kernel(KtTileArgs a) {
+    const int h = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (h >= a.heads) return;
+    const int8_t *q = a.q + h * 48;
+    const float scale = __fmul_rn(a.qs[h], 0.14433756729740643f);
+    float *sc = a.scores + (size_t)h * a.count;
+    float peak = -INFINITY;
+    for (int s = lane; s < a.count; s += 32) {
+        const int8_t *k = a.keys + (size_t)s * a.key_stride;
+        int dot = 0;
+        for (int d = 0; d < 48; d++) dot += (int)q[d] * (int)k[d];
+        const float v = __fmul_rn(__fmul_rn((float)dot, a.ks[(size_t)s * a.scale_stride]), scale);
+        sc[s] = v;
+        peak = fmaxf(peak, v);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) peak = fmaxf(peak, __shfl_xor_sync(0xffffffffu, peak, o));
+    for (int s = lane; s < a.count; s += 32) sc[s] = expf(__fsub_rn(sc[s], peak));
+    __syncwarp();
+    float total = 0.0f;
+    if (lane == 0)
+        for (int s = 0; s < a.count; s++) total = __fadd_rn(total, sc[s]);
+    total = __shfl_sync(0xffffffffu, total, 0);
+    const bool partial = a.peaks != nullptr;
+    if (!partial)
+        for (int s = lane; s < a.count; s += 32) sc[s] = __fdiv_rn(sc[s], total);
+    __syncwarp();
+    if (a.probs)
+        for (int s = lane; s < a.count; s += 32) a.probs[(size_t)h * a.count + s] = sc[s];
+    float o0 = 0.0f, o1 = 0.0f;
+    for (int s = 0; s < a.count; s++) {
+        const float w = __fmul_rn(sc[s], a.vs[(size_t)s * a.scale_stride]);
+        const int8_t *row = a.values + (size_t)s * a.value_stride;
+        o0 = __fadd_rn(o0, __fmul_rn(w, (float)row[2 * lane]));
+        o1 = __fadd_rn(o1, __fmul_rn(w, (float)row[2 * lane + 1]));
+    }
+    a.output[h * 64 + 2 * lane] = o0;
+    a.output[h * 64 + 2 * lane + 1] = o1;
+    if (partial && lane == 0) {
+        a.peaks[h] = peak;
+        a.sums[h] = total;
+    }
+}
+
+// Attention.MergePartials (src/Needle/Blocks.cs:750-817) over `count`
+// partial slots of 6*64 + 16 floats (outputs, peaks at 384 + h, sums at
+// 392 + h): warp per head, lane owns dims 2*lane, 2*lane+1, the scalar
+// branch's arithmetic (two-chunk form for count == 2).
+__global__ void __launch_bounds__(192) slot_merge_partials_kernel(const float *__restrict__ p, int count, int heads,
+                                                                  float *__restrict__ out) {
+    constexpr int kStride = 6 * 64 + 16, kPeak = 6 * 64;
+    const int h = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (h >= heads) return;
+    for (int k = 0; k < 2; k++) {
+        const int d = 2 * lane + k;
+        float r;
+        if (count == 2) {
+            const float p0 = p[kPeak + h], p1 = p[kStride + kPeak + h];
+            const float pk = fmaxf(p0, p1);
+            const float w0 = expf(__fsub_rn(p0, pk)), w1 = expf(__fsub_rn(p1, pk));
+            float tot = __fadd_rn(0.0f, __fmul_rn(w0, p[kPeak + 8 + h]));
+            tot = __fadd_rn(tot, __fmul_rn(w1, p[kStride + kPeak + 8 + h]));
+            const float inv = __fdiv_rn(1.0f, tot);
+            r = __fmul_rn(__fadd_rn(__fmul_rn(w0, p[h * 64 + d]), __fmul_rn(w1, p[kStride + h * 64 + d])), inv);
+        } else {
+            float peak = -INFINITY;
+            for (int c = 0; c < count; c++) peak = fmaxf(peak, p[c * kStride + kPeak + h]);
+            float total = 0.0f, sum = 0.0f;
+            for (int c = 0; c < count; c++) {
+                const float w = expf(__fsub_rn(p[c * kStride + kPeak + h], peak));
+                total = __fadd_rn(total, __fmul_rn(w, p[c * kStride + kPeak + 8 + h]));
+                sum = __fadd_rn(sum, __fmul_rn(w, p[c * kStride + h * 64 + d]));
+            }
+            r = __fmul_rn(sum, __fdiv_rn(1.0f, total));
+        }
+        out[h * 64 + d] = r;
+    }
+}
+
+int launch_slot_attention_tile(const KtTileArgs &a, cudaStream_t stream) {
+    slot_attention_tile_kernel<<<1, 192, 0, stream>>>(a);
+    return check_launch("slot_attention_tile");
+}
+int launch_slot_merge_partials(const float *partials, int count, int heads, float *out, cudaStream_t stream) {
+    slot_merge_partials_kernel<<<1, 192, 0, stream>>>(partials, count, heads, out);
+    return check_launch("slot_merge_partials");
+}
+
+// HadamardMlp.Apply (src/Needle/Blocks.cs:1067-1093, scalar steps
+// Scalar.cs:323-358,441-460) on one token: one CTA, each step's outputs in
+// parallel, every inner sum sequential in the scalar order.  w holds the
+// MlpWeights arrays (d1, d2, b2, d3, d4, w1a, w1b, w2a, w2b, w3a, w3b,
+// cond_v, cond_u); smem: weights[8], normalized[dim], front / back / kron
+// scratch [width] each.
+struct KtMlpArgs {
+    const float *w[13];
+    const float *pre_norm;
+    const int32_t *perm_a, *perm_b;
+    int dim, rows, cols;
+    float scale;
+    float *residual;
+};
+
+__device__ void mlp_kron(const float *z, int active_rows, const float *left, const float *right, int rows, int cols,
+                         int result_rows, float *tmp, float *result) {
+    for (int e = threadIdx.x; e < result_rows * cols; e += blockDim.x) {
+        const int k = e / cols, c = e - k * cols;
+        float sum = 0.0f;
+        for (int i = 0; i < active_rows; i++) sum = __fadd_rn(sum, __fmul_rn(left[i * rows + k], z[i * cols + c]));
+        tmp[e] = sum;
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < result_rows * cols; e += blockDim.x) {
+        const int k = e / cols, c = e - k * cols;
+        float sum = 0.0f;
+        for (int j = 0; j < cols; j++) sum = __fadd_rn(sum, __fmul_rn(tmp[k * cols + j], right[j * cols + c]));
+        result[e] = sum;
+    }
+    __syncthreads();
+}
+
+__global__ void __launch_bounds__(256) slot_hadamard_mlp_kernel(KtMlpArgs a) {
+    extern __shared__ float sm[];
+    const int dim = a.dim, rows = a.rows, cols = a.cols, width = rows * cols;
+    const int input_rows = (dim + cols - 1) / cols;
+    const int output_rows = min(rows, (input_rows + 3) / 4 * 4);
+    float *weights = sm, *normalized = sm + 8, *front = normalized + dim, *back = front + width, *tmp = back + width;
+    const float *d1 = a.w[0], *d2 = a.w[1], *b2 = a.w[2], *d3 = a.w[3], *d4 = a.w[4];
+    if (threadIdx.x == 0) {  // ZeroCenteredRms: the sum of squares in order
+        float sum = 0.0f;
+        for (int i = 0; i < dim; i++) sum = __fadd_rn(sum, __fmul_rn(a.residual[i], a.residual[i]));
+        weights[0] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, (float)dim), 1e-6f)));
+    }
+    __syncthreads();
+    const float inv = weights[0];
+    __syncthreads();
+    for (int i = threadIdx.x; i < dim; i += blockDim.x)
+        normalized[i] = __fmul_rn(__fmul_rn(__fadd_rn(1.0f, a.pre_norm[i]), a.residual[i]), inv);
+    __syncthreads();
+    if (threadIdx.x < 8) {  // ConditionWeights
+        float sum = 0.0f;
+        for (int i = 0; i < dim; i++) sum = __fadd_rn(sum, __fmul_rn(normalized[i], a.w[11][i * 8 + threadIdx.x]));
+        weights[threadIdx.x] = sum;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {  // Softmax over the 8 weights
+        float peak = -INFINITY, total = 0.0f;
+        for (int j = 0; j < 8; j++) peak = fmaxf(peak, weights[j]);
+        for (int j = 0; j < 8; j++) {
+            weights[j] = expf(__fsub_rn(weights[j], peak));
+            total = __fadd_rn(total, weights[j]);
+        }
+        for (int j = 0; j < 8; j++) weights[j] = __fdiv_rn(weights[j], total);
+    }
+    for (int i = threadIdx.x; i < input_rows * cols; i += blockDim.x)
+        front[i] = i < dim ? __fmul_rn(normalized[i], d1[i]) : 0.0f;
+    __syncthreads();
+    mlp_kron(front, input_rows, a.w[5], a.w[6], rows, cols, rows, tmp, back);
+    for (int n = threadIdx.x; n < width; n += blockDim.x) {
+        float condition = 1.0f;
+        for (int j = 0; j < 8; j++) condition = __fadd_rn(condition, __fmul_rn(weights[j], a.w[12][j * width + n]));
+        const float v = __fadd_rn(__fmul_rn(__fmul_rn(d2[n], condition), back[a.perm_a[n]]), b2[n]);
+        front[n] = __fmul_rn(v, __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-v))));
+    }
+    __syncthreads();
+    mlp_kron(front, rows, a.w[7], a.w[8], rows, cols, rows, tmp, back);
+    for (int n = threadIdx.x; n < width; n += blockDim.x) front[n] = __fmul_rn(back[a.perm_b[n]], d3[n]);
+    __syncthreads();
+    mlp_kron(front, rows, a.w[9], a.w[10], rows, cols, output_rows, tmp, back);
+    for (int i = threadIdx.x; i < dim; i += blockDim.x)
+        a.residual[i] = __fadd_rn(a.residual[i], __fmul_rn(a.scale, __fmul_rn(back[i], d4[i])));
+}
+
+int launch_slot_hadamard_mlp(const KtMlpArgs &a, cudaStream_t stream) {
+    const size_t smem = (size_t)(8 + a.dim + 3 * a.rows * a.cols) * 4;
+    if (smem > 200 * 1024) return set_error(NDL_ERR_UNSUPPORTED, "hadamard_mlp: dim %d x width %d too large", a.dim,
+                                            a.rows * a.cols);
+    cudaFuncSetAttribute(slot_hadamard_mlp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    slot_hadamard_mlp_kernel<<<1, 256, smem, stream>>>(a);
+    return check_launch("slot_hadamard_mlp");
+}
+
 static unsigned blocks_for(long long threads, int per_block) {
     return (unsigned)((threads + per_block - 1) / per_block);
 }

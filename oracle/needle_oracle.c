@@ -351,6 +351,60 @@ void ndo_post_norm_add(float *residual, const float *x, const float *scale, floa
     for (int i = 0; i < n; i++) residual[i] += gate * ((1.0f + scale[i]) * x[i] * inverse);
 }
 
+/* Scalar.Kron (Scalar.cs:441-460): result = left^T . z . right on a
+ * (rows x cols) grid, active input rows and result rows given. */
+static void kron(const float *z, int active_rows, const float *left, const float *right, int rows, int cols,
+                 int result_rows, float *result) {
+    float scratch[1024];
+    for (int k = 0; k < result_rows; k++) {
+        for (int c = 0; c < cols; c++) {
+            float sum = 0.0f;
+            for (int i = 0; i < active_rows; i++) sum += left[i * rows + k] * z[i * cols + c];
+            scratch[c] = sum;
+        }
+        for (int c = 0; c < cols; c++) {
+            float sum = 0.0f;
+            for (int j = 0; j < cols; j++) sum += scratch[j] * right[j * cols + c];
+            result[k * cols + c] = sum;
+        }
+    }
+}
+
+/* HadamardMlp.Apply, scalar path (src/Needle/Blocks.cs:1067-1093 with
+ * Scalar.ConditionWeights / ScaleInput / PermuteModulateActivate /
+ * PermuteScale / AccumulateOutput, Scalar.cs:323-358): the Kronecker-factored
+ * MLP on one token's residual, in place.  w: d1, d2, b2, d3, d4, w1a, w1b,
+ * w2a, w2b, w3a, w3b, cond_v, cond_u in MlpWeights order (Audio.cs:5-27). */
+void ndo_hadamard_mlp(const float *const *w, const float *pre_norm, const int32_t *perm_a, const int32_t *perm_b,
+                      int dim, int rows, int cols, float scale, float *residual) {
+    const float *d1 = w[0], *d2 = w[1], *b2 = w[2], *d3 = w[3], *d4 = w[4], *w1a = w[5], *w1b = w[6], *w2a = w[7],
+                *w2b = w[8], *w3a = w[9], *w3b = w[10], *cond_v = w[11], *cond_u = w[12];
+    int width = rows * cols;
+    int input_rows = (dim + cols - 1) / cols;
+    int output_rows = rows < (input_rows + 3) / 4 * 4 ? rows : (input_rows + 3) / 4 * 4;
+    float weights[8], normalized[8192], front[8192], back[8192];
+    ndo_zero_centered_rms(residual, pre_norm, dim, normalized);
+    for (int j = 0; j < 8; j++) {
+        float sum = 0.0f;
+        for (int i = 0; i < dim; i++) sum += normalized[i] * cond_v[i * 8 + j];
+        weights[j] = sum;
+    }
+    ndo_softmax(weights, 8);
+    for (int i = 0; i < dim; i++) front[i] = normalized[i] * d1[i];
+    for (int i = dim; i < input_rows * cols; i++) front[i] = 0.0f;
+    kron(front, input_rows, w1a, w1b, rows, cols, rows, back);
+    for (int n = 0; n < width; n++) {
+        float condition = 1.0f;
+        for (int j = 0; j < 8; j++) condition += weights[j] * cond_u[j * width + n];
+        float v = d2[n] * condition * back[perm_a[n]] + b2[n];
+        front[n] = v * ndo_sigmoid(v);
+    }
+    kron(front, rows, w2a, w2b, rows, cols, rows, back);
+    for (int n = 0; n < width; n++) front[n] = back[perm_b[n]] * d3[n];
+    kron(front, rows, w3a, w3b, rows, cols, output_rows, back);
+    for (int i = 0; i < dim; i++) residual[i] += scale * (back[i] * d4[i]);
+}
+
 /* ------------------------------------------------------------------------ */
 /* Quantized matmul                                                          */
 /* ------------------------------------------------------------------------ */

@@ -72,6 +72,8 @@ void ndo_rms_fake_a8(const float *x, int n, float *dst);
 void ndo_centered_rms_fake_a8(const float *x, const float *scale, int n, float *dst);
 void ndo_gate_fake_a8(float *x, const float *gate, int n);
 void ndo_post_norm_add(float *residual, const float *x, const float *scale, float gate, int n);
+void ndo_hadamard_mlp(const float *const *w, const float *pre_norm, const int32_t *perm_a, const int32_t *perm_b,
+                      int dim, int rows, int cols, float scale, float *residual); /* Blocks.cs:1067-1093 */
 void ndo_gather_row_cq(const uint8_t *indices, const uint16_t *norms, const float *levels, int cols, int bits, int row,
                        float *dst); /* Quant.cs:566-576 */
 

@@ -56,6 +56,7 @@ _SIGS = {
     "ndo_centered_rms_fake_a8": (None, [P, P, I, P]),
     "ndo_gate_fake_a8": (None, [P, P, I]),
     "ndo_post_norm_add": (None, [P, P, P, F, I]),
+    "ndo_hadamard_mlp": (None, [P, P, P, P, I, I, I, F, P]),
     "ndo_matmul_i8g32": (None, [P, P, I, I, P, P, I, P, P, I]),
     "ndo_attention_head": (None, [P, F, P, P, P, P, I, I, I, I, I, I, I, F, P, P, P]),
     "ndo_merge_partials": (None, [P, I, I, I, I, P]),
