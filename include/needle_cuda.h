@@ -374,6 +374,58 @@ NDL_API int ndl_taps3(const float *taps, int width, const float *triples, int n,
 NDL_API int ndl_fake_a8_rows(int mode, const float *x, const float *aux, const float *gate, int rows, int n,
                              float *dst, void *stream);
 
+/* Engram, the Needle-3 n-gram memory (EngineCore.ApplyEngramBatch,
+ * src/Needle/Engine.cs:2405-2469; EngramHashRowsBatch, :2652-2681), its own
+ * three steps on device memory (the table gather, fake-A8, prep and key /
+ * value matmuls are ndl_cq_gather_rows, ndl_kt_fake_a8's kernel, ndl_cq_prepare
+ * and ndl_cq_matmul).  Consecutive rows with the same slot form a run.
+ *   engram_hash  rows[t][table] (table = order index * heads + head) = the
+ *                table row of token t's n-gram, -1 while position < order - 1;
+ *                position = slot_length[slot] + offset in the run; tokens
+ *                before the run come from slot_prev[slot][0..1] (the slot's
+ *                last two, oldest first); orders: host array, 1..3 each.
+ *   engram_conv  out[t] = sum_j taps[j] * window[9 - j*dilation], j = 0..3,
+ *                window = the slot's 9 history values (history_in [slots][9]
+ *                [dim]) then the run's values; each run's slot gets its new
+ *                history in history_out (must not alias history_in).
+ *   engram_gate  residual[t] += sigmoid(dot(RmsUnit(x), RmsUnit(key)) /
+ *                sqrt(dim)) * v[t]. */
+NDL_API int ndl_engram_hash(const int32_t *tokens, const int32_t *row_slots, int count, const int32_t *slot_length,
+                            const int32_t *slot_prev, int slots, const int32_t *orders, int order_count, int heads,
+                            int engram_slots, int32_t *rows, void *stream);
+NDL_API int ndl_engram_conv(const float *history_in, const float *values, const int32_t *row_slots, int count,
+                            int slots, const float *taps, int dilation, int dim, float *out, float *history_out,
+                            void *stream);
+NDL_API int ndl_engram_gate(const float *x, const float *key, const float *v, int count, int dim, float *residual,
+                            void *stream);
+
+/* The Needle-3 confidence head (EngineCore.PoolTokensBatch,
+ * src/Needle/Engine.cs:2598-2650; ConfidenceLogitForSlot, :2702-2738) on
+ * caller-owned device state, pool_rows = (layers + 1) * probes per slot:
+ *   conf_pool_update  for layer row `row`: per token of each run (consecutive
+ *                     rows of one slot; a slot in at most one run per call),
+ *                     cell = mean of its 4 streams (streams [count][4][dim];
+ *                     stream 0 for a run's first token when initial), then per
+ *                     probe the online softmax of score = dot(cell, probe) /
+ *                     sqrt(dim) updates pool_max / pool_sum [slots][pool_rows]
+ *                     and pool_acc [slots][pool_rows][dim]; cell [slots][dim]
+ *                     keeps the run's last cell.  pending [slots] (nullable):
+ *                     a set slot first restores the row's pools from the
+ *                     snapshot arrays; the caller clears the flags.
+ *   conf_logit        per listed slot: logits[r] = bias + dot(pooled,
+ *                     projection) where pooled[q] = sum_i softmax_i(dot(k_i,
+ *                     query_q) / sqrt(dim) + row_bias[q][i]) * k_i and k_i =
+ *                     gain[i] * RmsUnit(pool_acc_i / pool_sum_i); pooled_out
+ *                     [n][queries][dim] nullable. */
+NDL_API int ndl_conf_pool_update(int row, const float *streams, const int32_t *row_slots, int count, int initial,
+                                 const float *probe_vectors, int probes, int dim, int pool_rows, int slots, float *cell,
+                                 float *pool_max, float *pool_sum, float *pool_acc, const float *snap_max,
+                                 const float *snap_sum, const float *snap_acc, const uint8_t *pending, void *stream);
+NDL_API int ndl_conf_logit(const int32_t *slot_list, int n, const float *pool_sum, const float *pool_acc,
+                           int pool_rows, int dim, const float *gain, const float *query_vectors,
+                           const float *row_bias, float bias, const float *projection, int queries, float *logits,
+                           float *pooled_out, void *stream);
+
 /* ------------------------------------------------------------------ */
 /* Batched decode engine (replaces BatchedEngine + EngineCore slots)   */
 /* ------------------------------------------------------------------ */

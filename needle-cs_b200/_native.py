@@ -110,6 +110,11 @@ SIGNATURES = {
     "ndl_hc_sinkhorn4x4": (c_int, [c_void_p, c_int, c_void_p, c_void_p]),
     "ndl_taps3": (c_int, [c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p]),
     "ndl_fake_a8_rows": (c_int, [c_int, c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p]),
+    "ndl_engram_hash": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p]),
+    "ndl_engram_conv": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p]),
+    "ndl_engram_gate": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p]),
+    "ndl_conf_pool_update": (c_int, [c_int, c_void_p, c_void_p, c_int, c_int, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
+    "ndl_conf_logit": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p, c_float, c_void_p, c_int, c_void_p, c_void_p, c_void_p]),
     "ndl_beam_search": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_void_p,
                                 c_void_p, c_void_p]),
     "ndl_sched_create": (c_int, [c_void_p, c_void_p, c_void_p]),

@@ -1,0 +1,183 @@
+// Engram, the Needle-3 n-gram memory (EngineCore.ApplyEngramBatch,
+// src/Needle/Engine.cs:2405-2469, and EngramHashRowsBatch, :2652-2681),
+// batched on the device.  The block's table gather, fake-A8, activation prep
+// and key / value matmuls are the CQ kernels (cq.cu) and the fake-A8 row op
+// (rowops.cu); this file holds the three steps that are Engram's own:
+//  * the row hash: per (token, table) an FNV-style hash of the token's
+//    n-gram (tokens of the same slot earlier in the batch, else the slot's
+//    last two tokens) picks a table row, -1 while the n-gram does not fit;
+//  * the causal conv: per token a window of the slot's last 9 values and its
+//    own, out = sum_j taps[j] * window[9 - j*dilation] over 4 taps; a run's
+//    last window becomes the slot's new history;
+//  * the gate: residual += sigmoid(dot(RmsUnit(x), RmsUnit(key)) / sqrt(dim)) * v.
+// Rows of consecutive tokens with the same slot form a run, as in the
+// reference's batch.  Integer work is exact; the float sums run in the
+// scalar code's order (the gate's exp aside).
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace ndl {
+
+constexpr int kEngramHistory = 9;  // EngineCore.EngramHistory (Engine.cs:27)
+constexpr int kEngramTaps = 4;     // EngineCore.EngramTaps (Engine.cs:28)
+constexpr int kEngramMaxOrders = 4;
+
+struct EngramOrders {
+    int v[kEngramMaxOrders];
+};
+
+__device__ __forceinline__ int run_first(const int32_t *row_slots, int t) {
+    int k = t;
+    while (k > 0 && row_slots[k - 1] == row_slots[t]) k--;
+    return k;
+}
+__device__ __forceinline__ int run_last(const int32_t *row_slots, int count, int t) {
+    int k = t;
+    while (k + 1 < count && row_slots[k + 1] == row_slots[t]) k++;
+    return k;
+}
+
+// Thread per (token, table).
+__global__ void __launch_bounds__(256) engram_hash_kernel(const int32_t *__restrict__ tokens,
+                                                          const int32_t *__restrict__ row_slots, int count,
+                                                          const int32_t *__restrict__ slot_length,
+                                                          const int32_t *__restrict__ slot_prev, int slots,
+                                                          EngramOrders orders, int order_count, int heads,
+                                                          int engram_slots, int32_t *__restrict__ rows) {
+    pdl_enter();
+    const int tables = order_count * heads;
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (long long)count * tables) return;
+    const int t = (int)(i / tables), table = (int)(i - (long long)t * tables);
+    const int slot = row_slots[t];
+    if (slot < 0 || slot >= slots) {
+        rows[i] = -1;
+        return;
+    }
+    const int rs = run_first(row_slots, t);
+    const int position = slot_length[slot] + t - rs;
+    const int order = orders.v[table / heads];
+    if (position < order - 1) {
+        rows[i] = -1;
+        return;
+    }
+    uint32_t acc = 0x9E3779B9u * (uint32_t)(table + 1);
+    for (int j = 0; j < order; j++) {
+        const int back = t - rs - j;
+        const int token = back >= 0 ? tokens[rs + back] : slot_prev[2 * slot + back + 2];
+        acc = (acc ^ (uint32_t)token) * 0x01000193u;
+    }
+    acc ^= acc >> 15;
+    rows[i] = table * engram_slots + (int)(acc % (uint32_t)engram_slots);
+}
+
+// Thread per (token, column).  The slot's value sequence is its 9 history
+// entries followed by the run's values; token t's window is entries
+// (t - run start) .. (t - run start) + 9 of it.
+__global__ void __launch_bounds__(256) engram_conv_kernel(const float *__restrict__ history_in,
+                                                          const float *__restrict__ values,
+                                                          const int32_t *__restrict__ row_slots, int count,
+                                                          int slots, const float *__restrict__ taps, int dilation,
+                                                          int dim, float *__restrict__ out,
+                                                          float *__restrict__ history_out) {
+    pdl_enter();
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (long long)count * dim) return;
+    const int t = (int)(i / dim), c = (int)(i - (long long)t * dim);
+    const int slot = row_slots[t];
+    if (slot < 0 || slot >= slots) {
+        out[(size_t)t * dim + c] = 0.0f;
+        return;
+    }
+    const int rs = run_first(row_slots, t), off = t - rs;
+    const float *hist = history_in + (size_t)slot * kEngramHistory * dim;
+    auto seq = [&](int p) { return p < kEngramHistory ? hist[(size_t)p * dim + c] : values[(size_t)(rs + p - kEngramHistory) * dim + c]; };
+    float acc = 0.0f;
+#pragma unroll
+    for (int j = 0; j < kEngramTaps; j++)
+        acc = __fadd_rn(acc, __fmul_rn(taps[(size_t)j * dim + c], seq(off + kEngramHistory - j * dilation)));
+    out[(size_t)t * dim + c] = acc;
+    if (t == run_last(row_slots, count, t)) {
+        float *ho = history_out + (size_t)slot * kEngramHistory * dim;
+        for (int k = 0; k < kEngramHistory; k++) ho[(size_t)k * dim + c] = seq(off + 1 + k);
+    }
+}
+
+// Warp per token; the sums of squares and the dot run on lane 0 in order.
+__global__ void __launch_bounds__(256) engram_gate_kernel(const float *__restrict__ x, const float *__restrict__ key,
+                                                          const float *__restrict__ v, int count, int dim,
+                                                          float *__restrict__ residual) {
+    pdl_enter();
+    const int t = (int)(((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
+    if (t >= count) return;
+    const float *xt = x + (size_t)t * dim, *kt = key + (size_t)t * dim;
+    float alpha = 0.0f;
+    if (lane == 0) {
+        float sa = 0.0f, sb = 0.0f;
+        for (int i = 0; i < dim; i++) {
+            sa = __fadd_rn(sa, __fmul_rn(xt[i], xt[i]));
+            sb = __fadd_rn(sb, __fmul_rn(kt[i], kt[i]));
+        }
+        const float ia = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sa, (float)dim), 1e-6f)));
+        const float ib = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sb, (float)dim), 1e-6f)));
+        float dot = 0.0f;
+        for (int i = 0; i < dim; i++) dot = __fadd_rn(dot, __fmul_rn(__fmul_rn(xt[i], ia), __fmul_rn(kt[i], ib)));
+        const float z = __fmul_rn(dot, __fdiv_rn(1.0f, __fsqrt_rn((float)dim)));
+        alpha = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-z)));
+    }
+    alpha = __shfl_sync(0xffffffffu, alpha, 0);
+    float *rt = residual + (size_t)t * dim;
+    const float *vt = v + (size_t)t * dim;
+    for (int i = lane; i < dim; i += 32) rt[i] = __fadd_rn(rt[i], __fmul_rn(alpha, vt[i]));
+}
+
+}  // namespace ndl
+
+using namespace ndl;
+
+extern "C" NDL_API int ndl_engram_hash(const int32_t *tokens, const int32_t *row_slots, int count,
+                                       const int32_t *slot_length, const int32_t *slot_prev, int slots,
+                                       const int32_t *orders, int order_count, int heads, int engram_slots,
+                                       int32_t *rows, void *stream) {
+    NDL_REQUIRE(count >= 0 && slots >= 1 && heads >= 1 && engram_slots >= 1, "count %d / slots %d / heads %d / rows %d",
+                count, slots, heads, engram_slots);
+    NDL_REQUIRE(orders && order_count >= 1 && order_count <= kEngramMaxOrders, "%d orders (1..%d)", order_count,
+                kEngramMaxOrders);
+    EngramOrders ov{};
+    for (int o = 0; o < order_count; o++) {
+        NDL_REQUIRE(orders[o] >= 1 && orders[o] <= 3, "order %d (1..3: two earlier tokens are kept per slot)",
+                    orders[o]);
+        ov.v[o] = orders[o];
+    }
+    NDL_REQUIRE((long long)order_count * heads * engram_slots <= 0x7FFFFFFF, "table rows overflow int");
+    if (count == 0) return NDL_OK;
+    NDL_REQUIRE(tokens && row_slots && slot_length && slot_prev && rows, "null pointer");
+    const long long n = (long long)count * order_count * heads;
+    launch_kernel(engram_hash_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, (cudaStream_t)stream, tokens,
+                  row_slots, count, slot_length, slot_prev, slots, ov, order_count, heads, engram_slots, rows);
+    return check_launch("engram_hash");
+}
+
+extern "C" NDL_API int ndl_engram_conv(const float *history_in, const float *values, const int32_t *row_slots,
+                                       int count, int slots, const float *taps, int dilation, int dim, float *out,
+                                       float *history_out, void *stream) {
+    NDL_REQUIRE(count >= 0 && slots >= 1 && dim >= 1, "count %d / slots %d / dim %d", count, slots, dim);
+    NDL_REQUIRE(dilation >= 1 && (kEngramTaps - 1) * dilation <= kEngramHistory, "dilation %d (1..3)", dilation);
+    if (count == 0) return NDL_OK;
+    NDL_REQUIRE(history_in && values && row_slots && taps && out && history_out, "null pointer");
+    NDL_REQUIRE(history_in != history_out, "history_out must not alias history_in");
+    const long long n = (long long)count * dim;
+    launch_kernel(engram_conv_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, (cudaStream_t)stream,
+                  history_in, values, row_slots, count, slots, taps, dilation, dim, out, history_out);
+    return check_launch("engram_conv");
+}
+
+extern "C" NDL_API int ndl_engram_gate(const float *x, const float *key, const float *v, int count, int dim,
+                                       float *residual, void *stream) {
+    NDL_REQUIRE(count >= 0 && dim >= 1, "count %d / dim %d", count, dim);
+    if (count == 0) return NDL_OK;
+    NDL_REQUIRE(x && key && v && residual, "null pointer");
+    launch_kernel(engram_gate_kernel, dim3((unsigned)((count * 32LL + 255) / 256)), dim3(256), 0,
+                  (cudaStream_t)stream, x, key, v, count, dim, residual);
+    return check_launch("engram_gate");
+}

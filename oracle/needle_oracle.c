@@ -406,6 +406,179 @@ void ndo_hadamard_mlp(const float *const *w, const float *pre_norm, const int32_
 }
 
 /* ------------------------------------------------------------------------ */
+/* Engram (Needle-3 n-gram memory)                                           */
+/* ------------------------------------------------------------------------ */
+
+/* EngineCore.EngramHashRowsBatch (src/Needle/Engine.cs:2652-2681): the table
+ * row of every (token, table) from the token's n-gram; rows of consecutive
+ * tokens of one slot form a run, earlier tokens come from the slot's last two
+ * (slot_prev[slot][0..1]), -1 before the n-gram fits.  rows [count][tables]. */
+void ndo_engram_hash(const int32_t *tokens, const int32_t *row_slots, int count, const int32_t *slot_length,
+                     const int32_t *slot_prev, const int32_t *orders, int order_count, int heads, int engram_slots,
+                     int32_t *rows) {
+    int tables = order_count * heads;
+    int run_start = 0;
+    for (int t = 0; t < count; t++) {
+        if (t == 0 || row_slots[t] != row_slots[t - 1]) run_start = t;
+        const int32_t *prev = slot_prev + 2 * row_slots[t];
+        int position = slot_length[row_slots[t]] + t - run_start;
+        for (int o = 0; o < order_count; o++)
+            for (int h = 0; h < heads; h++) {
+                int table = o * heads + h, order = orders[o];
+                if (position < order - 1) {
+                    rows[t * tables + table] = -1;
+                    continue;
+                }
+                uint32_t acc = 0x9E3779B9u * (uint32_t)(table + 1);
+                for (int j = 0; j < order; j++) {
+                    int back = t - run_start - j;
+                    int token = back >= 0 ? tokens[run_start + back] : prev[back + 2];
+                    acc = (acc ^ (uint32_t)token) * 0x01000193u;
+                }
+                acc ^= acc >> 15;
+                rows[t * tables + table] = table * engram_slots + (int)(acc % (uint32_t)engram_slots);
+            }
+    }
+}
+
+/* The causal conv of ApplyEngramBatch (src/Needle/Engine.cs:2421-2453): per
+ * token, a window of the slot's last 9 values and its own (history [slot][9]
+ * [dim], values [count][dim]); out = sum_j taps[j] * window[9 - j*dilation],
+ * j = 0..3 in order; a run's last window (minus its oldest entry) becomes the
+ * slot's new history (history_out). */
+void ndo_engram_conv(const float *history_in, const float *values, const int32_t *row_slots, int count,
+                     const float *taps, int dilation, int dim, float *out, float *history_out) {
+    enum { H = 9 };
+    float *stage = (float *)malloc(sizeof(float) * (size_t)(H + 1) * dim);
+    for (int rs = 0; rs < count;) {
+        int slot = row_slots[rs], rk = rs;
+        while (rk + 1 < count && row_slots[rk + 1] == slot) rk++;
+        memcpy(stage, history_in + (size_t)slot * H * dim, sizeof(float) * (size_t)H * dim);
+        for (int t = rs; t <= rk; t++) {
+            if (t > rs) memmove(stage, stage + dim, sizeof(float) * (size_t)H * dim);
+            memcpy(stage + (size_t)H * dim, values + (size_t)t * dim, sizeof(float) * (size_t)dim);
+            float *o = out + (size_t)t * dim;
+            for (int c = 0; c < dim; c++) o[c] = 0.0f;
+            for (int j = 0; j < 4; j++)
+                for (int c = 0; c < dim; c++) o[c] += taps[(size_t)j * dim + c] * stage[(size_t)(H - j * dilation) * dim + c];
+        }
+        memcpy(history_out + (size_t)slot * H * dim, stage + dim, sizeof(float) * (size_t)H * dim);
+        rs = rk + 1;
+    }
+    free(stage);
+}
+
+/* The gate of ApplyEngramBatch (src/Needle/Engine.cs:2455-2466), one token:
+ * residual += sigmoid(dot(RmsUnit(x), RmsUnit(key)) / sqrt(dim)) * v. */
+void ndo_engram_gate(const float *x, const float *key, const float *v, int dim, float *residual) {
+    float ia = ndo_inverse_rms(x, dim), ib = ndo_inverse_rms(key, dim);
+    float dot = 0.0f;
+    for (int i = 0; i < dim; i++) dot += (x[i] * ia) * (key[i] * ib);
+    float alpha = ndo_sigmoid(dot * (1.0f / sqrtf((float)dim)));
+    for (int i = 0; i < dim; i++) residual[i] += alpha * v[i];
+}
+
+/* ------------------------------------------------------------------------ */
+/* Confidence head (Needle-3 probe pooling)                                  */
+/* ------------------------------------------------------------------------ */
+
+static float dot_seq(const float *a, const float *b, int n) {
+    float s = 0.0f;
+    for (int i = 0; i < n; i++) s += a[i] * b[i];
+    return s;
+}
+
+/* EngineCore.PoolTokensBatch (src/Needle/Engine.cs:2598-2650) for one layer
+ * row: per token the slot's cell (the mean of the 4 streams, or stream 0 for
+ * the first token of an initial batch) scores against each probe, and the
+ * probe's online-softmax pool (max, sum, acc [dim]) absorbs it.  State per
+ * slot: cell [dim], pool_max / pool_sum [pool_rows], pool_acc [pool_rows][dim];
+ * with pending[slot] set, a run's first token first restores the probe's pool
+ * from the snapshot arrays. */
+void ndo_conf_pool_update(int row, const float *streams, const int32_t *row_slots, int count, int initial,
+                          const float *probe_vectors, int probes, int dim, int pool_rows, float *cell, float *pool_max,
+                          float *pool_sum, float *pool_acc, const float *snap_max, const float *snap_sum,
+                          const float *snap_acc, const uint8_t *pending) {
+    float inverse_root = 1.0f / sqrtf((float)dim);
+    float *c = (float *)malloc(sizeof(float) * (size_t)dim);
+    for (int rs = 0; rs < count;) {
+        int slot = row_slots[rs], rk = rs;
+        while (rk + 1 < count && row_slots[rk + 1] == slot) rk++;
+        memcpy(c, cell + (size_t)slot * dim, sizeof(float) * (size_t)dim);
+        float *mx = pool_max + (size_t)slot * pool_rows, *sm = pool_sum + (size_t)slot * pool_rows;
+        float *ac = pool_acc + (size_t)slot * pool_rows * dim;
+        int restore = pending && pending[slot];
+        for (int t = rs; t <= rk; t++) {
+            const float *st = streams + (size_t)t * 4 * dim;
+            if (initial && t == rs) memcpy(c, st, sizeof(float) * (size_t)dim);
+            else ndo_mix4(st, dim, 0.25f, 0.25f, 0.25f, 0.25f, c);
+            for (int pr = 0; pr < probes; pr++) {
+                int index = row * probes + pr;
+                float *acc = ac + (size_t)index * dim;
+                if (restore && t == rs) {
+                    mx[index] = snap_max[(size_t)slot * pool_rows + index];
+                    sm[index] = snap_sum[(size_t)slot * pool_rows + index];
+                    memcpy(acc, snap_acc + ((size_t)slot * pool_rows + index) * dim, sizeof(float) * (size_t)dim);
+                }
+                float score = dot_seq(c, probe_vectors + (size_t)index * dim, dim) * inverse_root;
+                if (score > mx[index]) {
+                    float rescale = expf(mx[index] - score);
+                    sm[index] = sm[index] * rescale + 1.0f;
+                    for (int i = 0; i < dim; i++) acc[i] = rescale * acc[i] + 1.0f * c[i];
+                    mx[index] = score;
+                } else {
+                    float weight = expf(score - mx[index]);
+                    sm[index] += weight;
+                    for (int i = 0; i < dim; i++) acc[i] += weight * c[i];
+                }
+            }
+        }
+        memcpy(cell + (size_t)slot * dim, c, sizeof(float) * (size_t)dim);
+        rs = rk + 1;
+    }
+    free(c);
+}
+
+/* EngineCore.ConfidenceLogitForSlot (src/Needle/Engine.cs:2702-2738) from a
+ * slot's pools (rows = pool_rows): each pooled mean, RMS-normalised and
+ * gained, forms the key of a row; each query attends over the rows
+ * (softmax of dot / sqrt(dim) + row bias) and the pooled queries project to
+ * the logit.  pooled_out [queries][dim] (nullable). */
+float ndo_conf_logit(const float *pool_sum, const float *pool_acc, int pool_rows, int dim, const float *gain,
+                     const float *query_vectors, const float *row_bias, float bias, const float *projection,
+                     int queries, float *pooled_out) {
+    float inverse_root = 1.0f / sqrtf((float)dim);
+    float *v = (float *)malloc(sizeof(float) * (size_t)pool_rows * dim);
+    float *w = (float *)malloc(sizeof(float) * (size_t)pool_rows);
+    float *pooled = (float *)malloc(sizeof(float) * (size_t)queries * dim);
+    for (int i = 0; i < pool_rows; i++) {
+        float *vi = v + (size_t)i * dim;
+        float inv_sum = 1.0f / pool_sum[i];
+        for (int k = 0; k < dim; k++) vi[k] = 0.0f * 0.0f + inv_sum * pool_acc[(size_t)i * dim + k];
+        float inv = ndo_inverse_rms(vi, dim);
+        for (int k = 0; k < dim; k++) vi[k] = vi[k] * inv;
+        for (int k = 0; k < dim; k++) vi[k] = gain[i] * vi[k] + 0.0f * vi[k];
+    }
+    float logit = bias;
+    for (int q = 0; q < queries; q++) {
+        for (int i = 0; i < pool_rows; i++)
+            w[i] = dot_seq(v + (size_t)i * dim, query_vectors + (size_t)q * dim, dim) * inverse_root +
+                   row_bias[q * pool_rows + i];
+        ndo_softmax(w, pool_rows);
+        float *pq = pooled + (size_t)q * dim;
+        for (int k = 0; k < dim; k++) pq[k] = 0.0f;
+        for (int i = 0; i < pool_rows; i++)
+            for (int k = 0; k < dim; k++) pq[k] += w[i] * v[(size_t)i * dim + k];
+    }
+    logit += dot_seq(pooled, projection, queries * dim);
+    if (pooled_out) memcpy(pooled_out, pooled, sizeof(float) * (size_t)queries * dim);
+    free(v);
+    free(w);
+    free(pooled);
+    return logit;
+}
+
+/* ------------------------------------------------------------------------ */
 /* Quantized matmul                                                          */
 /* ------------------------------------------------------------------------ */
 

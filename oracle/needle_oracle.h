@@ -72,6 +72,19 @@ void ndo_rms_fake_a8(const float *x, int n, float *dst);
 void ndo_centered_rms_fake_a8(const float *x, const float *scale, int n, float *dst);
 void ndo_gate_fake_a8(float *x, const float *gate, int n);
 void ndo_post_norm_add(float *residual, const float *x, const float *scale, float gate, int n);
+void ndo_engram_hash(const int32_t *tokens, const int32_t *row_slots, int count, const int32_t *slot_length,
+                     const int32_t *slot_prev, const int32_t *orders, int order_count, int heads, int engram_slots,
+                     int32_t *rows); /* Engine.cs:2652-2681 */
+void ndo_engram_conv(const float *history_in, const float *values, const int32_t *row_slots, int count,
+                     const float *taps, int dilation, int dim, float *out, float *history_out); /* Engine.cs:2421-2453 */
+void ndo_engram_gate(const float *x, const float *key, const float *v, int dim, float *residual); /* Engine.cs:2455-2466 */
+void ndo_conf_pool_update(int row, const float *streams, const int32_t *row_slots, int count, int initial,
+                          const float *probe_vectors, int probes, int dim, int pool_rows, float *cell, float *pool_max,
+                          float *pool_sum, float *pool_acc, const float *snap_max, const float *snap_sum,
+                          const float *snap_acc, const uint8_t *pending); /* Engine.cs:2598-2650 */
+float ndo_conf_logit(const float *pool_sum, const float *pool_acc, int pool_rows, int dim, const float *gain,
+                     const float *query_vectors, const float *row_bias, float bias, const float *projection,
+                     int queries, float *pooled_out); /* Engine.cs:2702-2738 */
 void ndo_hadamard_mlp(const float *const *w, const float *pre_norm, const int32_t *perm_a, const int32_t *perm_b,
                       int dim, int rows, int cols, float scale, float *residual); /* Blocks.cs:1067-1093 */
 void ndo_gather_row_cq(const uint8_t *indices, const uint16_t *norms, const float *levels, int cols, int bits, int row,

@@ -57,6 +57,11 @@ _SIGS = {
     "ndo_gate_fake_a8": (None, [P, P, I]),
     "ndo_post_norm_add": (None, [P, P, P, F, I]),
     "ndo_hadamard_mlp": (None, [P, P, P, P, I, I, I, F, P]),
+    "ndo_engram_hash": (None, [P, P, I, P, P, P, I, I, I, P]),
+    "ndo_engram_conv": (None, [P, P, P, I, P, I, I, P, P]),
+    "ndo_engram_gate": (None, [P, P, P, I, P]),
+    "ndo_conf_pool_update": (None, [I, P, P, I, I, P, I, I, I, P, P, P, P, P, P, P, P]),
+    "ndo_conf_logit": (F, [P, P, I, I, P, P, P, F, P, I, P]),
     "ndo_matmul_i8g32": (None, [P, P, I, I, P, P, I, P, P, I]),
     "ndo_attention_head": (None, [P, F, P, P, P, P, I, I, I, I, I, I, I, F, P, P, P]),
     "ndo_merge_partials": (None, [P, I, I, I, I, P]),
