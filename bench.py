@@ -67,6 +67,15 @@ class ClockSampler:
                  "-i", str(self.device_index)], stdout=self.file, stderr=subprocess.DEVNULL, text=True)
         except Exception:
             self.proc = None
+            return self
+        # nvidia-smi needs a moment before its first line; a short timed region
+        # would otherwise see no sample at all, so start only once it is live
+        deadline = time.time() + 5.0
+        while time.time() < deadline and self.proc.poll() is None:
+            self.file.flush()
+            if os.path.getsize(self.path) > 0:
+                break
+            time.sleep(0.01)
         return self
 
     def __exit__(self, *exc):
