@@ -300,7 +300,8 @@ __global__ void __launch_bounds__(256) attn_work_kernel(AttnArgs a) {
 
 // Persistent, warp-specialised.  The work list (rows sorted longest first,
 // heads and chunks of a row adjacent) is dealt dynamically: consumer warp w
-// takes item w first; after that, whenever its producer lane starts
+// takes item w first (its record and query scale loaded directly, as nothing
+// is in flight yet to hide them behind); after that, whenever its producer lane starts
 // issuing an item it claims the next unclaimed one from a counter in global
 // memory.  Warps that stream slower (the rate differs by SM and over time)
 // so take fewer items and the launch's warps finish together; claiming one
@@ -343,6 +344,15 @@ __device__ __forceinline__ void attn_producer(const AttnArgs &a, uint8_t *smem, 
     int fs = kClaimed, claim = blockIdx.x * kAttnConsumers + c;  // the first item is this warp's own
     long long t_issue = clock64() - kAttnLatencyCycles;
     unsigned fetches = 0;
+    if (!done) {  // the first record and scale load directly: nothing is in flight yet to hide them behind
+        if (claim < n_work) {
+            nx = a.work[claim];
+            qs_nx = __ldg(a.qs + (size_t)nx.row * a.heads + (nx.head_chunk & 0xFFFF));
+            fs = kReady;
+        } else {
+            fs = kExhausted;
+        }
+    }
     int k = 0, n_pages = 0;
     unsigned issued = 0;
     uint32_t idle = 0;
