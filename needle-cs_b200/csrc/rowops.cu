@@ -4,7 +4,7 @@
 // Hyper-connections (EngineCore.RunLayerBatch, src/Needle/Engine.cs:2352-2404):
 // a token carries 4 streams of `dim` floats.  Before the layer the streams
 // mix into the layer input (Mix4, Scalar.cs:255-258) and a 4x4 Sinkhorn
-// matrix (Scalar.Sinkhorn4x4, Scalar.cs:360-379) is made from the layer's
+// matrix (Scalar.Sinkhorn4x4, Scalar.cs:361-381) is made from the layer's
 // logits; after it, CombineDiff4x4 (Ops.cs:800-812) forms the next streams.
 // Conv taps: Scalar.Taps3 (Scalar.cs:285-288) over a (t-2, t-1, t) triple
 // (EngineCore.ChainTriple, Engine.cs:2471-2478).  Fake-A8 norms:

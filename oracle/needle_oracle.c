@@ -290,7 +290,7 @@ void ndo_taps3(const float *taps, int width, const float *current, float *dst) {
         dst[c] = taps[c] * current[c] + taps[width + c] * current[c - width] + taps[2 * width + c] * current[c - 2 * width];
 }
 
-/* Scalar.Sinkhorn4x4 (Scalar.cs:360-379): row-max exp, then 20 rounds of
+/* Scalar.Sinkhorn4x4 (Scalar.cs:361-381): row-max exp, then 20 rounds of
  * row and column normalisation (a column of zeros is left alone). */
 void ndo_sinkhorn4x4(const float *logits, float *result) {
     for (int r = 0; r < 4; r++) {
