@@ -115,6 +115,9 @@ struct ndl_engine {
     // rows, offsets, picks, probs (max_heads each) then ids and values
     void *d_sparse = nullptr, *h_sparse = nullptr;
     size_t sparse_bytes = 0;
+    // primed-prefix blob staging (grown on demand, kept across calls)
+    uint8_t *d_prefix = nullptr;
+    size_t prefix_bytes = 0;
     int last_rows = 0, last_heads = 0;
     int max_chunks_cap = 0;
     // captured step graphs, keyed by (rows, heads)
@@ -395,15 +398,44 @@ int check_status(ndl_engine *e) {
     return NDL_OK;
 }
 
+// Brings the device page table up to the host mirror for the entries that
+// `updates` (slot, page, value triples) names: per touched slot one copy of
+// the mirror's span from its lowest to its highest named page (the entries
+// between hold the mirror's values already).  Small and synchronous.
 int push_page_updates(ndl_engine *e, const std::vector<int32_t> &updates) {
     if (updates.empty()) return NDL_OK;
-    // apply on the host mirror's device copy directly: small, synchronous
+    std::vector<std::pair<int, std::pair<int, int>>> spans;  // slot -> [lo, hi]
     for (size_t i = 0; i < updates.size(); i += 3) {
-        NDL_CUDA(cudaMemcpyAsync(e->d_page_table + (size_t)updates[i] * e->max_pages + updates[i + 1],
-                                 e->page_table.data() + (size_t)updates[i] * e->max_pages + updates[i + 1],
-                                 sizeof(int32_t), cudaMemcpyHostToDevice, e->stream));
+        const int slot = updates[i], page = updates[i + 1];
+        auto it = std::find_if(spans.begin(), spans.end(), [&](const auto &s) { return s.first == slot; });
+        if (it == spans.end())
+            spans.push_back({slot, {page, page}});
+        else
+            it->second = {std::min(it->second.first, page), std::max(it->second.second, page)};
+    }
+    for (const auto &s : spans) {
+        const size_t at = (size_t)s.first * e->max_pages + s.second.first;
+        NDL_CUDA(cudaMemcpyAsync(e->d_page_table + at, e->page_table.data() + at,
+                                 sizeof(int32_t) * (size_t)(s.second.second - s.second.first + 1),
+                                 cudaMemcpyHostToDevice, e->stream));
     }
     NDL_CUDA(cudaStreamSynchronize(e->stream));
+    return NDL_OK;
+}
+
+// Device staging for one primed-prefix blob, kept across calls so that an
+// import or export does not allocate (and the pool does not trim) each time.
+static int prefix_reserve(ndl_engine *e, size_t bytes) {
+    if (bytes <= e->prefix_bytes) return NDL_OK;
+    NDL_CUDA(cudaStreamSynchronize(e->stream));
+    if (e->d_prefix) cudaFree(e->d_prefix);
+    e->d_prefix = nullptr;
+    e->prefix_bytes = 0;
+    if (cudaMalloc(reinterpret_cast<void **>(&e->d_prefix), bytes) != cudaSuccess) {
+        cudaGetLastError();
+        return set_error(NDL_ERR_OUT_OF_MEMORY, "primed prefix staging (%zu bytes)", bytes);
+    }
+    e->prefix_bytes = bytes;
     return NDL_OK;
 }
 
@@ -649,6 +681,7 @@ NDL_API int ndl_engine_destroy(ndl_engine *e) {
     if (e->h_out) cudaFreeHost(e->h_out);
     if (e->d_sparse) cudaFree(e->d_sparse);
     if (e->h_sparse) cudaFreeHost(e->h_sparse);
+    if (e->d_prefix) cudaFree(e->d_prefix);
     if (e->own_stream && e->stream) cudaStreamDestroy(e->stream);
     delete e;
     return NDL_OK;
@@ -1125,15 +1158,13 @@ NDL_API int ndl_slot_export_prefix(ndl_engine *e, int slot, void *blob, size_t b
     NDL_REQUIRE(bytes >= need, "primed prefix buffer too small (%zu bytes, %zu needed)", bytes, need);
     *static_cast<int32_t *>(blob) = len;
     if (len == 0) return NDL_OK;
-    uint8_t *stage = nullptr;
-    NDL_CUDA(cudaMallocAsync(reinterpret_cast<void **>(&stage), need, e->stream));
-    int st = launch_prefix_move(true, e->dc.layers, e->dc.heads, len, e->d_page_table + (size_t)slot * e->max_pages,
-                                e->pool, (long long)e->page_bytes, e->ec.kv_pages, stage, e->d_status, e->stream);
-    if (st == NDL_OK && cudaMemcpyAsync(static_cast<uint8_t *>(blob) + 4, stage + 4, need - 4, cudaMemcpyDeviceToHost,
-                                        e->stream) != cudaSuccess)
-        st = set_error(NDL_ERR_CUDA, "primed prefix download failed");
-    cudaFreeAsync(stage, e->stream);
-    TRY(st);
+    TRY(prefix_reserve(e, need));
+    uint8_t *stage = e->d_prefix;
+    TRY(launch_prefix_move(true, e->dc.layers, e->dc.heads, len, e->d_page_table + (size_t)slot * e->max_pages,
+                           e->pool, (long long)e->page_bytes, e->ec.kv_pages, stage, e->d_status, e->stream));
+    if (cudaMemcpyAsync(static_cast<uint8_t *>(blob) + 4, stage + 4, need - 4, cudaMemcpyDeviceToHost, e->stream) !=
+        cudaSuccess)
+        return set_error(NDL_ERR_CUDA, "primed prefix download failed");
     return check_status(e);
 }
 
@@ -1150,16 +1181,13 @@ NDL_API int ndl_slot_import_prefix(ndl_engine *e, int slot, const void *blob, si
     TRY(ndl_slot_reset(e, slot));
     if (len > 0) {
         TRY(reserve_pages(e, slot, 0, len));
-        uint8_t *stage = nullptr;
-        NDL_CUDA(cudaMallocAsync(reinterpret_cast<void **>(&stage), need, e->stream));
-        int st = cudaMemcpyAsync(stage, blob, need, cudaMemcpyHostToDevice, e->stream) == cudaSuccess
-                     ? launch_prefix_move(false, e->dc.layers, e->dc.heads, len,
-                                          e->d_page_table + (size_t)slot * e->max_pages, e->pool,
-                                          (long long)e->page_bytes, e->ec.kv_pages, stage, e->d_status, e->stream)
-                     : set_error(NDL_ERR_CUDA, "primed prefix upload failed");
-        cudaFreeAsync(stage, e->stream);
-        TRY(st);
-        TRY(check_status(e));
+        TRY(prefix_reserve(e, need));
+        uint8_t *stage = e->d_prefix;
+        if (cudaMemcpyAsync(stage, blob, need, cudaMemcpyHostToDevice, e->stream) != cudaSuccess)
+            return set_error(NDL_ERR_CUDA, "primed prefix upload failed");
+        TRY(launch_prefix_move(false, e->dc.layers, e->dc.heads, len, e->d_page_table + (size_t)slot * e->max_pages,
+                               e->pool, (long long)e->page_bytes, e->ec.kv_pages, stage, e->d_status, e->stream));
+        TRY(check_status(e));  // the blob is consumed once this returns
     }
     e->slot_len[slot] = len;
     e->slot_mark[slot] = len;
