@@ -669,6 +669,82 @@ NDL_API int ndl_sched_pending(ndl_sched *s, int *waiting, int *running);
 /* The last step's packing (arrays of max_rows, nullable). */
 NDL_API int ndl_sched_last_plan(ndl_sched *s, int *tokens, int *row_slots, int *rows, int *head_rows, int *heads);
 
+/* ---- Needle-3 model archive (.cact) -------------------------------------
+ * Replaces Model.FromBytes / FromMemory (src/Needle/Model.cs:307-404): the
+ * record table is walked in the reference's order and each tensor is named
+ * by its role and index (layer, site or probe head), e.g. "embedding" 0,
+ * "layer.q" l, "layer.mlp.cond_u" l, "hyper.phi_pre" 0, "hyper.perm_a" 0,
+ * "site.tables" s, "final_norm" 0, "manifest" 0, "probe.probe_vectors" h,
+ * "audio" k (an audio section's records, untyped).  The archive is checked
+ * with the reference's checks and messages: NDL_ERR_MALFORMED_MODEL where
+ * it throws InvalidDataException (short, wrong magic, truncated, a record
+ * of the wrong kind, no tokenizer) and NDL_ERR_UNSUPPORTED where it throws
+ * NotSupportedException (head, MLP and convolution geometry; more than 4
+ * orders or 16 sites).  Also malformed, where the reference reads out of
+ * range: a walk past the table, a tensor larger than its bytes, fewer than
+ * 28 codebook levels, a permutation entry outside [0, HadaN).
+ * device >= 0 uploads the weights to that device in one allocation:
+ *  - CQ codes and fp16 norms as stored, for ndl_cq_matmul / ndl_cq_gather_rows,
+ *    with a host codebook;
+ *  - dense tensors as fp32, converted by Scalar.HalfToSingle, or by
+ *    HalfToSingleUpstream before the audio section of an audio-carrying
+ *    archive;
+ *  - permutations as int32;
+ *  - the probe heads' CQ matrices also decoded to fp32 rows (Reader.Rows).
+ * device < 0 parses and checks on the host only.  The archive is not
+ * referenced after the call returns.  "layer.attn_gate" is the stored logit:
+ * the reference keeps its sigmoid. */
+typedef struct ndl_model ndl_model;
+enum {
+    NDL_TENSOR_DENSE = 0,       /* fp32 values [count] */
+    NDL_TENSOR_CQ = 1,          /* indices, norms, book; rows x cols, bits */
+    NDL_TENSOR_PERMUTATION = 2, /* int32 [count] */
+    NDL_TENSOR_CQ_ROWS = 3,     /* a CQ matrix and its decoded rows: values [rows][cols] */
+    NDL_TENSOR_RAW = 4
+};
+typedef struct {
+    uint32_t magic;
+    int tensors, codebook_entries;
+    int64_t length, tokenizer_bytes;
+    int has_audio, has_confidence, has_embedding_head;
+    int probe_heads, confidence_head, embedding_head; /* head indices, -1: none */
+    int probe_codes[16];                              /* ProbeHead codes: 1 embedding, 2 confidence, 3 router */
+    /* Geometry (src/Needle/Model.cs:65-120), header words 3..48 */
+    int vocab, dim, heads, kv_heads, layers, qk_dim, v_dim, max_seq, hada_n, lanes;
+    int sliding_window, conv_taps, engram_slots, engram_sub, engram_tables;
+    int engram_conv_taps, engram_dilation, engram_seed_heads, kv_window;
+    int order_count, site_count;
+    uint64_t global_mask;
+    float rope_theta;
+    int orders[4], sites[16];
+    int hada_rows, hada_cols;
+    int device; /* -1: host only */
+    size_t device_bytes;
+} ndl_model_info;
+typedef struct {
+    int kind, record, dtype, ndim;
+    int64_t shape[4];
+    uint64_t offset, bytes; /* the record's bytes in the archive */
+    int64_t count;          /* elements of values / permutation */
+    int rows, cols, bits;   /* CQ */
+    /* device addresses after an upload (NULL otherwise) */
+    const float *values;
+    const int32_t *permutation;
+    const uint8_t *indices;
+    const uint16_t *norms;
+    const ndl_kt_codebook *book; /* host */
+} ndl_model_tensor;
+NDL_API int ndl_model_load(const void *archive, size_t bytes, int device, ndl_model **out);
+NDL_API int ndl_model_destroy(ndl_model *m);
+NDL_API int ndl_model_get_info(const ndl_model *m, ndl_model_info *info);
+NDL_API int ndl_model_tensor_count(const ndl_model *m, int *count);
+NDL_API int ndl_model_tensor_name(const ndl_model *m, int i, const char **role, int *index);
+NDL_API int ndl_model_get_tensor(const ndl_model *m, const char *role, int index, ndl_model_tensor *t);
+/* The host copy of a dense (fp32) or permutation (int32) tensor. */
+NDL_API int ndl_model_read_host(const ndl_model *m, const char *role, int index, void *destination, size_t bytes);
+/* The tokenizer record's bytes (owned by the model). */
+NDL_API int ndl_model_tokenizer(const ndl_model *m, const void **blob, size_t *bytes);
+
 #ifdef __cplusplus
 }
 #endif

@@ -129,6 +129,14 @@ SIGNATURES = {
     "ndl_engine_use_graphs": (c_int, [c_void_p, c_int]),
     "ndl_engine_use_pdl": (c_int, [c_void_p, c_int]),
     "ndl_engine_profile_read": (c_int, [c_void_p, c_void_p, c_void_p, c_int]),
+    "ndl_model_load": (c_int, [c_void_p, c_size_t, c_int, c_void_p]),
+    "ndl_model_destroy": (c_int, [c_void_p]),
+    "ndl_model_get_info": (c_int, [c_void_p, c_void_p]),
+    "ndl_model_tensor_count": (c_int, [c_void_p, ctypes.POINTER(c_int)]),
+    "ndl_model_tensor_name": (c_int, [c_void_p, c_int, ctypes.POINTER(c_char_p), ctypes.POINTER(c_int)]),
+    "ndl_model_get_tensor": (c_int, [c_void_p, c_char_p, c_int, c_void_p]),
+    "ndl_model_read_host": (c_int, [c_void_p, c_char_p, c_int, c_void_p, c_size_t]),
+    "ndl_model_tokenizer": (c_int, [c_void_p, ctypes.POINTER(c_void_p), ctypes.POINTER(c_size_t)]),
 }
 
 PROF_CLASSES = ["prepare", "norm_quant", "gemm_qkv", "kv_write", "attention", "gemm_o", "gemm_gateup", "swiglu",

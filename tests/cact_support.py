@@ -1,0 +1,161 @@
+"""Writes small synthetic Needle-3 archives (.cact) for the loader tests.
+
+The layout is the reference's (src/Needle/Model.cs:191-198, 307-361):
+ * a 196-byte header of uint32 words (magic, record count, codebook entries,
+   then the Geometry words 3..48, word 48 the fp32 RoPE theta);
+ * the codebook levels (fp32);
+ * the record table (44-byte records: dtype, ndim, pad, 4 shape words,
+   offset, bytes, group, bits);
+ * the tensor bytes, with the tokenizer blob as the last record.
+Tensors follow the Reader's order: embedding, each layer (LayerWeights + MlpWeights),
+the hyper-connections, the Engram sites, the final norm, then either probe
+heads (manifest + ProbeHead) or an audio section.  Shapes are small and
+only as constrained as the loader checks them.
+"""
+import struct
+
+import numpy as np
+
+MAGIC = 0x05E12A84
+HEADER_BYTES = 196
+FP16, FP32, CQ, RAW = 1, 2, 3, 4
+
+GEOMETRY = dict(kv_window=64, vocab=256, dim=128, heads=2, kv_heads=1, layers=2, qk_dim=48, v_dim=64, max_seq=512,
+                hada_n=128, lanes=4, sliding_window=64, global_mask=0b10, conv_taps=3, engram_slots=97,
+                engram_sub=1, engram_tables=4, engram_conv_taps=4, engram_dilation=2, engram_seed_heads=2,
+                orders=[2, 3], sites=[1], rope_theta=10000.0)
+WORDS = dict(kv_window=3, vocab=5, dim=7, heads=8, kv_heads=9, layers=10, qk_dim=11, v_dim=12, max_seq=13, hada_n=14,
+             lanes=15, sliding_window=16, conv_taps=19, engram_slots=20, engram_sub=21, engram_tables=22,
+             engram_conv_taps=23, engram_dilation=24, engram_seed_heads=25)
+
+LAYER = ["layer.norm_in", ("layer.q", 96), ("layer.k", 48), ("layer.v", 64), "layer.q_taps", "layer.k_taps",
+         "layer.v_taps", "layer.q_norm", "layer.k_norm", ("layer.gate", 128), ("layer.out", 128), "layer.post_norm",
+         "layer.attn_gate", "layer.pre_hada"] + ["layer.mlp." + n for n in (
+             "d1", "d2", "b2", "d3", "d4", "w1a", "w1b", "w2a", "w2b", "w3a", "w3b", "cond_v", "cond_u")]
+
+
+def half_to_single(halves, exact=True):
+    """Scalar.HalfToSingle / HalfToSingleUpstream (src/Needle/Scalar.cs:113-128) on uint16 words."""
+    h = np.asarray(halves, np.uint16).astype(np.uint32)
+    mag = h & 0x7FFF
+    bits = ((mag << 13) + 0x38000000) | ((h & 0x8000) << 16)
+    out = bits.astype(np.uint32).view(np.float32).copy()
+    if exact:
+        sub = (mag > 0) & (mag < 0x400)
+        v = mag[sub].astype(np.float32) * np.float32(5.9604645e-8)
+        out[sub] = np.where(h[sub] & 0x8000, -v, v)
+    out[mag == 0] = 0.0
+    return out
+
+
+class Archive:
+    """Collects records in order; ``build()`` returns the archive bytes."""
+
+    def __init__(self, seed=0, geometry=None):
+        self.rng = np.random.default_rng(seed)
+        self.g = dict(GEOMETRY, **(geometry or {}))
+        self.records = []  # (role, index, dtype, shape, payload bytes, bits, expected)
+        levels = np.zeros(28, np.float32)
+        levels[0:4] = [-1.5, -0.5, 0.5, 1.5]
+        levels[12:28] = np.linspace(-2.0, 2.0, 16).astype(np.float32) * 0.75
+        self.levels = levels
+
+    def dense(self, role, index, n, fp16=True, values=None):
+        if fp16:
+            raw = (np.asarray(values, np.uint16) if values is not None
+                   else self.rng.normal(0, 1, n).astype(np.float16).view(np.uint16))
+            self.records.append((role, index, FP16, [raw.size], raw.tobytes(), 0, ("dense16", raw)))
+        else:
+            v = np.asarray(values, np.float32) if values is not None else self.rng.normal(0, 1, n).astype(np.float32)
+            self.records.append((role, index, FP32, [v.size], v.tobytes(), 0, ("dense32", v)))
+
+    def cq(self, role, index, rows, cols, bits):
+        codes = self.rng.integers(0, 256, rows * cols * bits // 8, dtype=np.uint8)
+        norms = self.rng.uniform(0.01, 0.2, rows * (cols // 128)).astype(np.float16).view(np.uint16)
+        self.records.append((role, index, CQ, [rows, cols], codes.tobytes() + norms.tobytes(), bits,
+                             ("cq", codes, norms, rows, cols, bits)))
+
+    def perm(self, role, n, values=None):
+        p = np.asarray(values if values is not None else self.rng.permutation(n), np.float32)
+        self.records.append((role, 0, FP32, [p.size], p.tobytes(), 0, ("perm", p.astype(np.int32))))
+
+    def raw(self, payload):
+        self.records.append(("tokenizer", 0, RAW, [len(payload)], payload, 0, ("raw", payload)))
+
+    def standard(self, probe_codes=(2,), audio=False, final_norm=None):
+        """A full archive in the Reader's order."""
+        g = self.g
+        d = g["dim"]
+        self.cq("embedding", 0, g["vocab"], d, 4)
+        for layer in range(g["layers"]):
+            for item in LAYER:
+                if isinstance(item, tuple):
+                    self.cq(item[0], layer, item[1], d, 2)
+                elif item == "layer.attn_gate":
+                    self.dense(item, layer, 1, fp16=False)
+                else:
+                    self.dense(item, layer, 24, fp16=layer % 2 == 0)
+        for n in ("a_pre", "a_post", "a_res", "b_pre", "b_post", "b_res"):
+            self.dense("hyper." + n, 0, 16)
+        for n in ("phi_pre", "phi_post", "phi_res"):
+            self.cq("hyper." + n, 0, 24, 4 * d, 2)
+        if g["hada_n"] > 0:
+            self.perm("hyper.perm_a", g["hada_n"])
+            self.perm("hyper.perm_b", g["hada_n"])
+        for s in range(len(g["sites"])):
+            self.cq("site.tables", s, g["engram_tables"] * g["engram_slots"], d, 4)
+            self.cq("site.key", s, d, d, 2)
+            self.cq("site.value", s, d, d, 2)
+            self.dense("site.taps", s, 4 * d)
+        if final_norm is not None:
+            self.dense("final_norm", 0, None, values=final_norm)
+        else:
+            self.dense("final_norm", 0, d)
+        if audio:
+            self.dense("audio", 0, 13, fp16=False)
+            self.cq("audio", 1, 8, d, 4)
+            self.dense("audio", 2, 40)
+        elif probe_codes:
+            self.dense("manifest", 0, None, fp16=False, values=np.array(probe_codes, np.float32))
+            for h, code in enumerate(probe_codes):
+                rows = g["layers"] + 1
+                self.cq("probe.probe_vectors", h, rows * 2, d, 4)
+                self.dense("probe.gain", h, rows * 2)
+                self.cq("probe.query_vectors", h, 2, d, 4)
+                self.dense("probe.row_bias", h, 2 * rows * 2)
+                self.cq("probe.projection", h, 1, 2 * d, 4)
+                self.dense("probe.bias", h, 1)
+                if code == 3:
+                    self.dense("probe.router", h, 5)
+        self.raw(b"needle tokenizer blob \x00\x01\x02")
+        return self
+
+    def header_words(self):
+        g = self.g
+        h = np.zeros(HEADER_BYTES // 4, np.uint32)
+        h[0], h[1], h[2] = MAGIC, len(self.records), self.levels.size
+        for k, w in WORDS.items():
+            h[w] = g[k]
+        h[17], h[18] = g["global_mask"] & 0xFFFFFFFF, g["global_mask"] >> 32
+        h[26] = len(g["orders"])
+        h[27:27 + len(g["orders"])] = g["orders"]
+        h[31] = len(g["sites"])
+        h[32:32 + len(g["sites"])] = g["sites"]
+        h[48] = np.array([g["rope_theta"]], np.float32).view(np.uint32)[0]
+        return h
+
+    def build(self, header=None):
+        h = self.header_words() if header is None else header
+        table_at = HEADER_BYTES + self.levels.size * 4
+        at = table_at + 44 * len(self.records)
+        table, blobs = b"", b""
+        for _, _, dtype, shape, payload, bits, _ in self.records:
+            at = (at + 15) // 16 * 16
+            pad = at - (table_at + 44 * len(self.records) + len(blobs))
+            blobs += b"\x00" * pad
+            shape4 = list(shape) + [0] * (4 - len(shape))
+            table += struct.pack("<BBH4IQQII", dtype, len(shape), 0, *shape4, at, len(payload),
+                                 128 if dtype == CQ else 0, bits)
+            blobs += payload
+            at += len(payload)
+        return h.tobytes() + self.levels.tobytes() + table + blobs
