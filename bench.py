@@ -31,7 +31,7 @@ FALLBACK_HBM_GBS = 6650.0
 # (needle-cs_b200/profile_case.py attention: 321.5 MB for 298.2 MB); the
 # excess is the unused tail of each row's last 64-position page, so traffic
 # grows with the algorithmic bytes and scales to the 12-layer launch.
-ATTN_TRAFFIC_PER_ALG_BYTE = 1.078
+ATTN_TRAFFIC_PER_ALG_BYTE = 1.076
 
 
 def hbm_peak():
