@@ -745,6 +745,31 @@ NDL_API int ndl_model_read_host(const ndl_model *m, const char *role, int index,
 /* The tokenizer record's bytes (owned by the model). */
 NDL_API int ndl_model_tokenizer(const ndl_model *m, const void **blob, size_t *bytes);
 
+/* The Engram block of one site on a loaded model (EngineCore.ApplyEngramBatch,
+ * src/Needle/Engine.cs:2405-2469), chained on `stream` over `count` tokens:
+ *   rows = the n-gram hash rows (ndl_engram_hash, the model's orders, heads
+ *          and table size);
+ *   e[t] = FakeA8 of [GatherRow(site.tables, rows[t][0]) | ... ] (a -1 row
+ *          gathers zeros);
+ *   key, value = site.key / site.value times e prepared at 2 bits (CQ);
+ *   conv = the dilated 4-tap conv of value over the slot's 9-entry history
+ *          (ndl_engram_conv: history_out gets the batch slots' new
+ *          histories, other slots' entries are left as they are);
+ *   residual[t] += sigmoid(dot(RmsUnit(x[t]), RmsUnit(key[t])) / sqrt(dim)) * conv[t].
+ * tokens, row_slots [count]; slot_length [slots]; slot_prev [slots][2];
+ * history_in / history_out [slots][9][dim] (this site's); x, residual
+ * [count][dim]: device memory.  workspace: device memory of at least
+ * ndl_engram_workspace(m, count) bytes, 256-byte aligned.  The model must be
+ * on a device; its tables must tile the input (EngramTables x EngramSub ==
+ * Dim) and its key / value matrices be 2-bit Dim x Dim, else
+ * NDL_ERR_UNSUPPORTED.  Bars: bit-exact to the scalar chain up to the gate,
+ * whose sigmoid goes through CUDA's expf. */
+NDL_API size_t ndl_engram_workspace(const ndl_model *m, int count);
+NDL_API int ndl_engram_apply(const ndl_model *m, int site, const int32_t *tokens, const int32_t *row_slots, int count,
+                             const int32_t *slot_length, const int32_t *slot_prev, int slots, const float *history_in,
+                             float *history_out, const float *x, float *residual, void *workspace,
+                             size_t workspace_bytes, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -131,6 +131,54 @@ __global__ void __launch_bounds__(256) engram_gate_kernel(const float *__restric
     for (int i = lane; i < dim; i += 32) rt[i] = __fadd_rn(rt[i], __fmul_rn(alpha, vt[i]));
 }
 
+// Quant.FakeA8 (src/Needle/Quant.cs:69-80) per row, warp per row: the row's
+// peak, then each value quantized with the reference's RoundEven (the
+// 1.5 * 2^23 bias, which also turns -0 into +0) and scaled back.
+__global__ void __launch_bounds__(256) engram_fake_a8_kernel(float *__restrict__ x, int rows, int n) {
+    pdl_enter();
+    const int r = (int)(((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
+    if (r >= rows) return;
+    float *row = x + (size_t)r * n;
+    float peak = 0.0f;
+    for (int i = lane; i < n; i += 32) peak = fmaxf(peak, fabsf(row[i]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) peak = fmaxf(peak, __shfl_xor_sync(0xffffffffu, peak, o));
+    const float scale = peak > 0.0f ? __fdiv_rn(peak, 127.0f) : 1.0f;
+    const float inverse = __fdiv_rn(1.0f, scale);
+    for (int i = lane; i < n; i += 32) {
+        const float q = __fsub_rn(__fadd_rn(__fmul_rn(row[i], inverse), 12582912.0f), 12582912.0f);
+        row[i] = __fmul_rn(fminf(fmaxf(q, -128.0f), 127.0f), scale);
+    }
+}
+
+// Workspace of ndl_engram_apply, 256-byte aligned pieces.
+struct EngramWork {
+    size_t rows, e, values, scales, offsets, key, value, conv, total;
+    int stride;
+};
+EngramWork engram_work(int count, int tables, int dim) {
+    EngramWork w{};
+    size_t end = 0;
+    auto place = [&](size_t bytes) {
+        end = (end + 255) & ~(size_t)255;
+        const size_t at = end;
+        end += bytes;
+        return at;
+    };
+    const size_t rd = (size_t)count * dim;
+    w.stride = ((dim / 128) + 7) & ~7;
+    w.rows = place((size_t)count * tables * 4);
+    w.e = place(rd * 4);
+    w.values = place(rd);
+    w.scales = place((size_t)count * w.stride * 4);
+    w.offsets = place((size_t)count * w.stride * 4);
+    w.key = place(rd * 4);
+    w.value = place(rd * 4);
+    w.conv = place(rd * 4);
+    w.total = (end + 255) & ~(size_t)255;
+    return w;
+}
+
 }  // namespace ndl
 
 using namespace ndl;
@@ -180,4 +228,86 @@ extern "C" NDL_API int ndl_engram_gate(const float *x, const float *key, const f
     launch_kernel(engram_gate_kernel, dim3((unsigned)((count * 32LL + 255) / 256)), dim3(256), 0,
                   (cudaStream_t)stream, x, key, v, count, dim, residual);
     return check_launch("engram_gate");
+}
+
+// The Engram block of one site on a loaded model (ApplyEngramBatch,
+// src/Needle/Engine.cs:2405-2469), chained on the stream:
+//  row hash -> table rows gathered (GatherRow; -1 gives zeros) into
+//  e[t] = [table 0 | table 1 | ...] -> FakeA8 per row -> 2-bit CQ prep ->
+//  key and value CQ matmuls -> dilated conv over the slot history ->
+//  residual += sigmoid(dot(RmsUnit(x), RmsUnit(key)) / sqrt(dim)) * conv.
+static int engram_site_views(const ndl_model *m, int site, ndl_model_info *g, ndl_model_tensor *tables,
+                             ndl_model_tensor *key, ndl_model_tensor *value, ndl_model_tensor *taps) {
+    NDL_REQUIRE(m, "null model");
+    if (ndl_model_get_info(m, g) != NDL_OK) return NDL_ERR_INVALID_ARG;
+    NDL_REQUIRE(site >= 0 && site < g->site_count, "site %d of %d", site, g->site_count);
+    NDL_REQUIRE(g->device >= 0, "the model is not on a device (load it with a device)");
+    if (ndl_model_get_tensor(m, "site.tables", site, tables) != NDL_OK ||
+        ndl_model_get_tensor(m, "site.key", site, key) != NDL_OK ||
+        ndl_model_get_tensor(m, "site.value", site, value) != NDL_OK ||
+        ndl_model_get_tensor(m, "site.taps", site, taps) != NDL_OK)
+        return NDL_ERR_INVALID_ARG;
+    const int dim = g->dim, heads = g->order_count > 0 ? g->engram_tables / g->order_count : 0;
+    if (g->order_count < 1 || heads * g->order_count != g->engram_tables || g->engram_tables * g->engram_sub != dim ||
+        tables->cols != g->engram_sub || tables->rows != g->engram_tables * g->engram_slots)
+        return set_error(NDL_ERR_UNSUPPORTED,
+                         "Engram site %d: %d tables of %d columns (%d x %d rows) do not tile the %d-wide input", site,
+                         g->engram_tables, tables->cols, g->engram_tables, g->engram_slots, dim);
+    if (key->bits != 2 || value->bits != 2 || key->rows != dim || key->cols != dim || value->rows != dim ||
+        value->cols != dim || taps->count < 4LL * dim)
+        return set_error(NDL_ERR_UNSUPPORTED, "Engram site %d: key / value must be 2-bit %d x %d, taps 4 x %d", site,
+                         dim, dim, dim);
+    return NDL_OK;
+}
+
+extern "C" NDL_API size_t ndl_engram_workspace(const ndl_model *m, int count) {
+    ndl_model_info g;
+    if (!m || count < 0 || ndl_model_get_info(m, &g) != NDL_OK) return 0;
+    return engram_work(count, g.engram_tables, g.dim).total;
+}
+
+extern "C" NDL_API int ndl_engram_apply(const ndl_model *m, int site, const int32_t *tokens, const int32_t *row_slots,
+                                        int count, const int32_t *slot_length, const int32_t *slot_prev, int slots,
+                                        const float *history_in, float *history_out, const float *x, float *residual,
+                                        void *workspace, size_t workspace_bytes, void *stream) {
+    ndl_model_info g;
+    ndl_model_tensor tables, key, value, taps;
+    const int st = engram_site_views(m, site, &g, &tables, &key, &value, &taps);
+    if (st != NDL_OK) return st;
+    NDL_REQUIRE(count >= 0 && slots >= 1, "count %d / slots %d", count, slots);
+    if (count == 0) return NDL_OK;
+    const int dim = g.dim;
+    const EngramWork w = engram_work(count, g.engram_tables, dim);
+    NDL_REQUIRE(workspace && workspace_bytes >= w.total, "workspace of %zu bytes, %zu needed", workspace_bytes,
+                w.total);
+    NDL_REQUIRE(((uintptr_t)workspace & 255) == 0, "workspace must be 256-byte aligned");
+    uint8_t *ws = static_cast<uint8_t *>(workspace);
+    int32_t *rows = reinterpret_cast<int32_t *>(ws + w.rows);
+    float *e = reinterpret_cast<float *>(ws + w.e), *scales = reinterpret_cast<float *>(ws + w.scales);
+    float *offsets = reinterpret_cast<float *>(ws + w.offsets), *k = reinterpret_cast<float *>(ws + w.key);
+    float *v = reinterpret_cast<float *>(ws + w.value), *conv = reinterpret_cast<float *>(ws + w.conv);
+    int8_t *values = reinterpret_cast<int8_t *>(ws + w.values);
+    const int heads = g.engram_tables / g.order_count;
+#define ENGRAM_TRY(x)                      \
+    do {                                   \
+        const int s_ = (x);                \
+        if (s_ != NDL_OK) return s_;       \
+    } while (0)
+    ENGRAM_TRY(ndl_engram_hash(tokens, row_slots, count, slot_length, slot_prev, slots, g.orders, g.order_count, heads,
+                               g.engram_slots, rows, stream));
+    ENGRAM_TRY(ndl_cq_gather_rows(tables.indices, tables.norms, tables.book->levels, tables.rows, tables.cols,
+                                  tables.bits, rows, count * g.engram_tables, e, stream));
+    launch_kernel(engram_fake_a8_kernel, dim3((unsigned)((count * 32LL + 255) / 256)), dim3(256), 0,
+                  (cudaStream_t)stream, e, count, dim);
+    ENGRAM_TRY(check_launch("engram_fake_a8"));
+    ENGRAM_TRY(ndl_cq_prepare(e, count, dim, 2, values, scales, offsets, w.stride, stream));
+    ENGRAM_TRY(ndl_cq_matmul(key.indices, key.norms, key.book->bytes, key.book->byte_scale, dim, dim, 2, values,
+                             scales, offsets, w.stride, count, k, dim, 0, dim, stream));
+    ENGRAM_TRY(ndl_cq_matmul(value.indices, value.norms, value.book->bytes, value.book->byte_scale, dim, dim, 2,
+                             values, scales, offsets, w.stride, count, v, dim, 0, dim, stream));
+    ENGRAM_TRY(ndl_engram_conv(history_in, v, row_slots, count, slots, taps.values, g.engram_dilation, dim, conv,
+                               history_out, stream));
+    ENGRAM_TRY(ndl_engram_gate(x, k, conv, count, dim, residual, stream));
+#undef ENGRAM_TRY
+    return NDL_OK;
 }

@@ -103,7 +103,8 @@ class Archive:
             self.perm("hyper.perm_a", g["hada_n"])
             self.perm("hyper.perm_b", g["hada_n"])
         for s in range(len(g["sites"])):
-            self.cq("site.tables", s, g["engram_tables"] * g["engram_slots"], d, 4)
+            sub = g["engram_sub"] if g["engram_sub"] % 128 == 0 else d  # tables tile the input when sub allows
+            self.cq("site.tables", s, g["engram_tables"] * g["engram_slots"], sub, 4)
             self.cq("site.key", s, d, d, 2)
             self.cq("site.value", s, d, d, 2)
             self.dense("site.taps", s, 4 * d)
