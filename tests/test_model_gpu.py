@@ -7,7 +7,9 @@ with the host rule, permutations exactly.  The probe heads' decoded rows
 GatherRow bit for bit.  The model's tensors then drive the device kernels
 directly, each checked bit for bit against the oracle:
  * an embedding gather (ndl_cq_gather_rows on "embedding");
- * a CQ matmul (ndl_cq_matmul on "layer.gate" 1 with the model's codebook).
+ * a CQ matmul (ndl_cq_matmul on "layer.gate" 1 with the model's codebook);
+ * the confidence head (ndl_conf_pool_update and ndl_conf_logit on the
+   probe head's tensors), to the oracle's tolerance for its exp.
 """
 import ctypes
 
@@ -109,3 +111,60 @@ def test_model_tensors_drive_the_kernels(loaded, oracle):
     want = oracle.matmul_rows_cq(exp[1].reshape(w.rows, -1), exp[2].reshape(w.rows, -1), obook, w.bits, vals, sc, off)
     torch.cuda.synchronize()
     assert np.array_equal(y.cpu().numpy().view(np.uint32), want.view(np.uint32))
+
+
+def test_confidence_head_runs_on_model_weights(loaded, oracle):
+    """The n7 kernels (ndl_conf_pool_update, ndl_conf_logit) fed by the
+    model's confidence head: decoded probe, query and projection rows, gain,
+    row bias and bias, against the oracle on the same tensors."""
+    import torch
+
+    from needle_cs_b200 import _native
+
+    cact, a, m = loaded
+    info = m.info
+    h = info["confidence_head"]
+    assert h == 0
+    probes_t, query_t, proj_t = (m.tensor(r, h) for r in ("probe.probe_vectors", "probe.query_vectors",
+                                                          "probe.projection"))
+    dim, layers = info["dim"], info["layers"]
+    pool_rows, queries = probes_t.rows, query_t.rows
+    probes = pool_rows // (layers + 1)
+    rows_of = lambda t: _read(t.values, t.rows * t.cols, "<f4", np.float32).reshape(t.rows, t.cols)
+    probe_v, qv, proj = rows_of(probes_t), rows_of(query_t), rows_of(proj_t).reshape(-1)
+    gain, rb, bias = m.host("probe.gain", h), m.host("probe.row_bias", h), float(m.host("probe.bias", h)[0])
+    rng = np.random.default_rng(41)
+    slots = 6
+    row_slots = np.array([3, 3, 1, 4, 4, 4], np.int32)
+    count = row_slots.size
+    cell = np.zeros((slots, dim), np.float32)
+    pmax = np.full((slots, pool_rows), -np.inf, np.float32)
+    psum = np.zeros((slots, pool_rows), np.float32)
+    pacc = np.zeros((slots, pool_rows, dim), np.float32)
+    want = [x.copy() for x in (cell, pmax, psum, pacc)]
+    dev = torch.device("cuda:0")
+    d = {k: torch.from_numpy(v).to(dev) for k, v in dict(cell=cell, pmax=pmax, psum=psum, pacc=pacc,
+                                                          rs=row_slots).items()}
+    olib = oracle.lib()
+    for row in range(layers + 1):
+        streams = rng.normal(size=(count, 4, dim)).astype(np.float32)
+        olib.ndo_conf_pool_update(row, streams.ctypes.data, row_slots.ctypes.data, count, int(row == 0),
+                                  probe_v.ctypes.data, probes, dim, pool_rows, want[0].ctypes.data,
+                                  want[1].ctypes.data, want[2].ctypes.data, want[3].ctypes.data, None, None, None,
+                                  None)
+        ds = torch.from_numpy(streams).to(dev)
+        _native.call("ndl_conf_pool_update", row, ds.data_ptr(), d["rs"].data_ptr(), count, int(row == 0),
+                     probes_t.values, probes, dim, pool_rows, slots, d["cell"].data_ptr(), d["pmax"].data_ptr(),
+                     d["psum"].data_ptr(), d["pacc"].data_ptr(), None, None, None, None, None)
+    listed = np.array([3, 1, 4], np.int32)
+    dl = torch.from_numpy(listed).to(dev)
+    logits = torch.empty(listed.size, device=dev)
+    _native.call("ndl_conf_logit", dl.data_ptr(), listed.size, d["psum"].data_ptr(), d["pacc"].data_ptr(), pool_rows,
+                 dim, m.tensor("probe.gain", h).values, query_t.values, m.tensor("probe.row_bias", h).values, bias,
+                 proj_t.values, queries, logits.data_ptr(), None, None)
+    got = logits.cpu().numpy()
+    for r, s in enumerate(listed):
+        wp = np.zeros((queries, dim), np.float32)
+        wl = olib.ndo_conf_logit(want[2][s].ctypes.data, want[3][s].ctypes.data, pool_rows, dim, gain.ctypes.data,
+                                 qv.ctypes.data, rb.ctypes.data, bias, proj.ctypes.data, queries, wp.ctypes.data)
+        assert abs(got[r] - wl) <= 1e-5 * max(1.0, abs(wl)), (r, got[r], wl)
