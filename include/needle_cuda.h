@@ -764,6 +764,14 @@ NDL_API int ndl_model_tokenizer(const ndl_model *m, const void **blob, size_t *b
  * Dim) and its key / value matrices be 2-bit Dim x Dim, else
  * NDL_ERR_UNSUPPORTED.  Bars: bit-exact to the scalar chain up to the gate,
  * whose sigmoid goes through CUDA's expf. */
+/* HadamardMlp.Apply (src/Needle/Blocks.cs:1067-1093) on `count` residual
+ * rows [count][Dim] (device memory, updated in place) with layer `layer`'s
+ * MLP factors and pre-norm scale and the model's two permutations; `scale`
+ * as MlpBatch.Scale.  One block per row, the same kernel as the KernelTable
+ * slot (inner sums in the scalar order; the condition softmax and the SiLU
+ * through expf, tolerance).  A tensor shorter than the HadaRows x HadaCols
+ * split needs is NDL_ERR_UNSUPPORTED. */
+NDL_API int ndl_mlp_apply(const ndl_model *m, int layer, float *residual, int count, float scale, void *stream);
 NDL_API size_t ndl_engram_workspace(const ndl_model *m, int count);
 NDL_API int ndl_engram_apply(const ndl_model *m, int site, const int32_t *tokens, const int32_t *row_slots, int count,
                              const int32_t *slot_length, const int32_t *slot_prev, int slots, const float *history_in,

@@ -138,6 +138,7 @@ SIGNATURES = {
     "ndl_model_read_host": (c_int, [c_void_p, c_char_p, c_int, c_void_p, c_size_t]),
     "ndl_model_tokenizer": (c_int, [c_void_p, ctypes.POINTER(c_void_p), ctypes.POINTER(c_size_t)]),
     "ndl_engram_workspace": (c_size_t, [c_void_p, c_int]),
+    "ndl_mlp_apply": (c_int, [c_void_p, c_int, c_void_p, c_int, c_float, c_void_p]),
     "ndl_engram_apply": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_int, c_void_p,
                                  c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
 }

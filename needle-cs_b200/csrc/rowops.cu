@@ -374,6 +374,7 @@ struct KtMlpArgs {
     int dim, rows, cols;
     float scale;
     float *residual;
+    long long row_stride;  // block b updates residual + b * row_stride (0: one row)
 };
 
 __device__ void mlp_kron(const float *z, int active_rows, const float *left, const float *right, int rows, int cols,
@@ -396,6 +397,7 @@ __device__ void mlp_kron(const float *z, int active_rows, const float *left, con
 
 __global__ void __launch_bounds__(256) slot_hadamard_mlp_kernel(KtMlpArgs a) {
     extern __shared__ float sm[];
+    float *const residual = a.residual + (size_t)blockIdx.x * a.row_stride;
     const int dim = a.dim, rows = a.rows, cols = a.cols, width = rows * cols;
     const int input_rows = (dim + cols - 1) / cols;
     const int output_rows = min(rows, (input_rows + 3) / 4 * 4);
@@ -403,14 +405,14 @@ __global__ void __launch_bounds__(256) slot_hadamard_mlp_kernel(KtMlpArgs a) {
     const float *d1 = a.w[0], *d2 = a.w[1], *b2 = a.w[2], *d3 = a.w[3], *d4 = a.w[4];
     if (threadIdx.x == 0) {  // ZeroCenteredRms: the sum of squares in order
         float sum = 0.0f;
-        for (int i = 0; i < dim; i++) sum = __fadd_rn(sum, __fmul_rn(a.residual[i], a.residual[i]));
+        for (int i = 0; i < dim; i++) sum = __fadd_rn(sum, __fmul_rn(residual[i], residual[i]));
         weights[0] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, (float)dim), 1e-6f)));
     }
     __syncthreads();
     const float inv = weights[0];
     __syncthreads();
     for (int i = threadIdx.x; i < dim; i += blockDim.x)
-        normalized[i] = __fmul_rn(__fmul_rn(__fadd_rn(1.0f, a.pre_norm[i]), a.residual[i]), inv);
+        normalized[i] = __fmul_rn(__fmul_rn(__fadd_rn(1.0f, a.pre_norm[i]), residual[i]), inv);
     __syncthreads();
     if (threadIdx.x < 8) {  // ConditionWeights
         float sum = 0.0f;
@@ -443,7 +445,7 @@ __global__ void __launch_bounds__(256) slot_hadamard_mlp_kernel(KtMlpArgs a) {
     __syncthreads();
     mlp_kron(front, rows, a.w[9], a.w[10], rows, cols, output_rows, tmp, back);
     for (int i = threadIdx.x; i < dim; i += blockDim.x)
-        a.residual[i] = __fadd_rn(a.residual[i], __fmul_rn(a.scale, __fmul_rn(back[i], d4[i])));
+        residual[i] = __fadd_rn(residual[i], __fmul_rn(a.scale, __fmul_rn(back[i], d4[i])));
 }
 
 int launch_slot_hadamard_mlp(const KtMlpArgs &a, cudaStream_t stream) {
@@ -548,4 +550,57 @@ extern "C" NDL_API int ndl_fake_a8_rows(int mode, const float *x, const float *a
     if (rows == 0) return NDL_OK;
     NDL_REQUIRE(x && dst && (mode == 0 || aux) && (mode != 3 || gate), "null pointer");
     return launch_fake_a8(mode, x, aux, gate, rows, n, dst, (cudaStream_t)stream);
+}
+
+// HadamardMlp.Apply (src/Needle/Blocks.cs:1067-1093) over `count` residual
+// rows of a loaded model's layer, block per row: the layer's MLP factors and
+// pre-norm scale, the model's two permutations, its HadaRows x HadaCols split.
+extern "C" NDL_API int ndl_mlp_apply(const ndl_model *m, int layer, float *residual, int count, float scale,
+                                     void *stream) {
+    NDL_REQUIRE(m, "null model");
+    ndl_model_info g;
+    if (ndl_model_get_info(m, &g) != NDL_OK) return NDL_ERR_INVALID_ARG;
+    NDL_REQUIRE(g.device >= 0, "the model is not on a device (load it with a device)");
+    NDL_REQUIRE(layer >= 0 && layer < g.layers, "layer %d of %d", layer, g.layers);
+    NDL_REQUIRE(count >= 0, "count %d", count);
+    const int dim = g.dim, rows = g.hada_rows, cols = g.hada_cols, width = g.hada_n;
+    const int in_rows = cols > 0 ? (dim + cols - 1) / cols : 0;
+    if (width <= 0 || in_rows > rows)
+        return set_error(NDL_ERR_UNSUPPORTED, "HadaN %d (%d x %d) cannot hold a %d-wide row", width, rows, cols, dim);
+    static const char *names[13] = {"layer.mlp.d1",  "layer.mlp.d2",  "layer.mlp.b2",     "layer.mlp.d3",
+                                    "layer.mlp.d4",  "layer.mlp.w1a", "layer.mlp.w1b",    "layer.mlp.w2a",
+                                    "layer.mlp.w2b", "layer.mlp.w3a", "layer.mlp.w3b",    "layer.mlp.cond_v",
+                                    "layer.mlp.cond_u"};
+    const long long need[13] = {dim, width, width, width, dim, (long long)in_rows * rows, (long long)cols * cols,
+                                (long long)rows * rows, (long long)cols * cols, (long long)rows * rows,
+                                (long long)cols * cols, (long long)dim * 8, 8LL * width};
+    KtMlpArgs a{};
+    ndl_model_tensor t;
+    for (int k = 0; k < 13; k++) {
+        if (ndl_model_get_tensor(m, names[k], layer, &t) != NDL_OK) return NDL_ERR_INVALID_ARG;
+        if (t.kind != NDL_TENSOR_DENSE || t.count < need[k])
+            return set_error(NDL_ERR_UNSUPPORTED, "%s %d holds %lld values, %lld needed", names[k], layer,
+                             (long long)t.count, need[k]);
+        a.w[k] = t.values;
+    }
+    if (ndl_model_get_tensor(m, "layer.pre_hada", layer, &t) != NDL_OK) return NDL_ERR_INVALID_ARG;
+    if (t.count < dim) return set_error(NDL_ERR_UNSUPPORTED, "layer.pre_hada %d holds %lld values", layer, (long long)t.count);
+    a.pre_norm = t.values;
+    if (ndl_model_get_tensor(m, "hyper.perm_a", 0, &t) != NDL_OK) return NDL_ERR_INVALID_ARG;
+    a.perm_a = t.permutation;
+    if (ndl_model_get_tensor(m, "hyper.perm_b", 0, &t) != NDL_OK) return NDL_ERR_INVALID_ARG;
+    a.perm_b = t.permutation;
+    if (count == 0) return NDL_OK;
+    NDL_REQUIRE(residual, "null residual");
+    a.dim = dim;
+    a.rows = rows;
+    a.cols = cols;
+    a.scale = scale;
+    a.residual = residual;
+    a.row_stride = dim;
+    const size_t smem = (size_t)(8 + dim + 3 * width) * 4;
+    if (smem > 200 * 1024) return set_error(NDL_ERR_UNSUPPORTED, "hadamard_mlp: dim %d x width %d too large", dim, width);
+    NDL_CUDA(cudaFuncSetAttribute(slot_hadamard_mlp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    slot_hadamard_mlp_kernel<<<(unsigned)count, 256, smem, (cudaStream_t)stream>>>(a);
+    return check_launch("hadamard_mlp_rows");
 }

@@ -94,7 +94,7 @@ class Archive:
                 elif item == "layer.attn_gate":
                     self.dense(item, layer, 1, fp16=False)
                 else:
-                    self.dense(item, layer, 24, fp16=layer % 2 == 0)
+                    self.dense(item, layer, self._layer_size(item), fp16=layer % 2 == 0)
         for n in ("a_pre", "a_post", "a_res", "b_pre", "b_post", "b_res"):
             self.dense("hyper." + n, 0, 16)
         for n in ("phi_pre", "phi_post", "phi_res"):
@@ -130,6 +130,20 @@ class Archive:
                     self.dense("probe.router", h, 5)
         self.raw(b"needle tokenizer blob \x00\x01\x02")
         return self
+
+    def _layer_size(self, role):
+        """Sizes of the MLP factors for the HadaRows x HadaCols split (HadamardMlp.Apply), else 24."""
+        g = self.g
+        d, width = g["dim"], g["hada_n"]
+        rows = 1 << ((width - 1).bit_length() // 2) if width > 0 else 1
+        cols = width // rows if width > 0 else 1
+        in_rows = (d + cols - 1) // cols
+        sizes = {"d1": d, "d2": width, "b2": width, "d3": width, "d4": d, "w1a": in_rows * rows, "w1b": cols * cols,
+                 "w2a": rows * rows, "w2b": cols * cols, "w3a": rows * rows, "w3b": cols * cols, "cond_v": d * 8,
+                 "cond_u": 8 * width}
+        if role == "layer.pre_hada":
+            return d
+        return sizes.get(role.rsplit(".", 1)[1], 24) if role.startswith("layer.mlp.") else 24
 
     def header_words(self):
         g = self.g

@@ -168,3 +168,35 @@ def test_confidence_head_runs_on_model_weights(loaded, oracle):
         wl = olib.ndo_conf_logit(want[2][s].ctypes.data, want[3][s].ctypes.data, pool_rows, dim, gain.ctypes.data,
                                  qv.ctypes.data, rb.ctypes.data, bias, proj.ctypes.data, queries, wp.ctypes.data)
         assert abs(got[r] - wl) <= 1e-5 * max(1.0, abs(wl)), (r, got[r], wl)
+
+
+def test_kronecker_mlp_runs_on_model_weights(loaded, oracle):
+    """ndl_mlp_apply over several residual rows of a layer against the oracle's
+    HadamardMlp restatement on the same (host) tensors, to the KernelTable
+    slot's bar (2e-5 of the update: the condition softmax and the SiLU go
+    through expf)."""
+    import torch
+
+    from needle_cs_b200 import _native
+
+    cact, a, m = loaded
+    info = m.info
+    dim, rows, cols = info["dim"], info["hada_rows"], info["hada_cols"]
+    names = ["d1", "d2", "b2", "d3", "d4", "w1a", "w1b", "w2a", "w2b", "w3a", "w3b", "cond_v", "cond_u"]
+    rng = np.random.default_rng(51)
+    for layer in range(info["layers"]):
+        host = [np.ascontiguousarray(m.host("layer.mlp." + n, layer)) for n in names]
+        pre = m.host("layer.pre_hada", layer)
+        pa, pb = m.host("hyper.perm_a"), m.host("hyper.perm_b")
+        residual = rng.normal(size=(5, dim)).astype(np.float32)
+        want = residual.copy()
+        ptrs = (ctypes.c_void_p * 13)(*[h.ctypes.data for h in host])
+        for t in range(5):
+            oracle.lib().ndo_hadamard_mlp(ptrs, pre.ctypes.data, pa.ctypes.data, pb.ctypes.data, dim, rows, cols,
+                                          0.5, want[t].ctypes.data)
+        res = torch.from_numpy(residual).cuda()
+        _native.call("ndl_mlp_apply", m._h, layer, res.data_ptr(), 5, 0.5, None)
+        got = res.cpu().numpy()
+        delta = np.abs(want - residual).max()
+        assert delta > 1e-3  # the MLP moves the rows
+        assert np.abs(got - want).max() <= 2e-5 * max(1.0, float(delta)), np.abs(got - want).max()
