@@ -220,3 +220,11 @@ def test_cq_larger_than_its_bytes_is_malformed(cact):
 def test_missing_file_raises_file_not_found(cact, tmp_path):
     with pytest.raises(FileNotFoundError):
         cact.Model.open(str(tmp_path / "absent.cact"))
+
+
+def test_upload_to_a_missing_device_is_an_error(cact):
+    """A device index no GPU answers to fails with NDL_ERR_NO_DEVICE and no model."""
+    a = Archive(seed=11).standard()
+    with pytest.raises(cact.NeedleError) as e:
+        cact.Model.from_bytes(a.build(), device=4096)
+    assert e.value.status == 106 and "no CUDA device 4096" in str(e.value)
