@@ -141,6 +141,35 @@ class Model:
         call("ndl_model_tokenizer", self._h, ctypes.byref(blob), ctypes.byref(n))
         return ctypes.string_at(blob, n.value) if n.value else b""
 
+    # -- blocks on the uploaded weights (torch CUDA tensors, contiguous) --
+    def engram_workspace_bytes(self, count):
+        return int(lib().ndl_engram_workspace(self._h, count))
+
+    def apply_engram(self, site, tokens, row_slots, slot_length, slot_prev, history_in, history_out, x, residual,
+                     workspace=None):
+        """ApplyEngramBatch for one site on torch's current stream: residual
+        [count][dim] updated, history_out [slots][9][dim] gets the batch
+        slots' new histories (ndl_engram_apply)."""
+        import torch
+
+        count = int(row_slots.numel())
+        if workspace is None:
+            workspace = torch.empty(self.engram_workspace_bytes(count), dtype=torch.uint8, device=residual.device)
+        call("ndl_engram_apply", self._h, site, tokens.data_ptr(), row_slots.data_ptr(), count,
+             slot_length.data_ptr(), slot_prev.data_ptr(), int(slot_length.numel()), history_in.data_ptr(),
+             history_out.data_ptr(), x.data_ptr(), residual.data_ptr(), workspace.data_ptr(), workspace.numel(),
+             torch.cuda.current_stream().cuda_stream)
+        return residual
+
+    def apply_mlp(self, layer, residual, scale):
+        """HadamardMlp.Apply over the rows of residual [count][dim], in place,
+        on torch's current stream (ndl_mlp_apply)."""
+        import torch
+
+        call("ndl_mlp_apply", self._h, layer, residual.data_ptr(), int(residual.shape[0]), float(scale),
+             torch.cuda.current_stream().cuda_stream)
+        return residual
+
     def close(self):
         if getattr(self, "_h", None):
             lib().ndl_model_destroy(self._h)

@@ -94,12 +94,15 @@ def test_engram_block_matches_the_scalar_chain(pkg, cuda, oracle):
         need = _native.lib().ndl_engram_workspace(m._h, count)
         assert need > 0
         ws = torch.empty(need, dtype=torch.uint8, device=dev)
-        for _ in range(2):
+        for call in range(3):  # two calls through the C ABI on one workspace, one through the mirror
             res = torch.from_numpy(residual).to(dev)
             hout = d["hist"].clone()
-            _native.call("ndl_engram_apply", m._h, 0, d["tok"].data_ptr(), d["rs"].data_ptr(), count,
-                         d["sl"].data_ptr(), d["sp"].data_ptr(), slots, d["hist"].data_ptr(), hout.data_ptr(),
-                         d["x"].data_ptr(), res.data_ptr(), ws.data_ptr(), need, None)
+            if call < 2:
+                _native.call("ndl_engram_apply", m._h, 0, d["tok"].data_ptr(), d["rs"].data_ptr(), count,
+                             d["sl"].data_ptr(), d["sp"].data_ptr(), slots, d["hist"].data_ptr(), hout.data_ptr(),
+                             d["x"].data_ptr(), res.data_ptr(), ws.data_ptr(), need, None)
+            else:
+                m.apply_engram(0, d["tok"], d["rs"], d["sl"], d["sp"], d["hist"], hout, d["x"], res)
             torch.cuda.synchronize()
             assert np.array_equal(hout.cpu().numpy().view(np.uint32), want_hist.view(np.uint32))
             got = res.cpu().numpy()

@@ -195,7 +195,7 @@ def test_kronecker_mlp_runs_on_model_weights(loaded, oracle):
             oracle.lib().ndo_hadamard_mlp(ptrs, pre.ctypes.data, pa.ctypes.data, pb.ctypes.data, dim, rows, cols,
                                           0.5, want[t].ctypes.data)
         res = torch.from_numpy(residual).cuda()
-        _native.call("ndl_mlp_apply", m._h, layer, res.data_ptr(), 5, 0.5, None)
+        m.apply_mlp(layer, res, 0.5)
         got = res.cpu().numpy()
         delta = np.abs(want - residual).max()
         assert delta > 1e-3  # the MLP moves the rows
