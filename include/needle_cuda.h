@@ -166,7 +166,9 @@ NDL_API int ndl_matmul_i8g32_batched(const int8_t *q, const float *sa, int m, co
  * 512-position chunks merged afterwards; the chunk partials live in
  * `workspace` (NULL: allocated and freed on `stream` by the library).
  * status (nullable, device int) receives 2 for an out-of-range slot, page
- * or length and 1 for a timed-out wait; those rows are skipped. */
+ * or length and 1 for a timed-out wait.  A row with an out-of-range slot or
+ * length, and a head whose pages include one outside the pool, is skipped
+ * and its out values are NaN; after a timed-out wait out is undefined. */
 NDL_API size_t ndl_attention_paged_workspace(int rows, int heads, int max_pages);
 NDL_API int ndl_attention_paged(const int8_t *q, const float *qs, const int32_t *row_slot, const int32_t *row_pos,
                                 int rows, int heads, const int32_t *page_table, int slots, int max_pages,
@@ -178,10 +180,12 @@ NDL_API int ndl_attention_paged(const int8_t *q, const float *qs, const int32_t 
  * (frame-budgeted game or job threads, audio callbacks, zero-allocation
  * request loops), where cudaMalloc could block or synchronise the device.
  * Same arguments and results as ndl_attention_paged, without a workspace:
- * the chunk partials live in a 4 MiB device array owned by the library
- * (held on every GPU that loads it until exit).  Requests whose workspace
- * (ndl_attention_paged_workspace) exceeds 4 MiB are rejected with
- * NDL_ERR_INVALID_ARG.  The first call on a device looks the array up
+ * the chunk partials and the work list live in a 4 MiB device array owned
+ * by the library (held on every GPU that loads it until exit).  Requests
+ * whose ndl_attention_paged_workspace(rows, heads, max_pages) exceeds 4 MiB
+ * are rejected with NDL_ERR_INVALID_ARG: each (row, head, 512-position
+ * chunk) takes 320 bytes, so rows * heads * ceil(max_pages / 8) may be at
+ * most 13107 (512 rows x 8 heads x 3 chunks = 1536 positions fit).  The first call on a device looks the array up
  * (cudaGetSymbolAddress) and must come before any stream capture.  All
  * calls share the array: calls that overlap on the GPU race and must be
  * ordered by the caller (e.g. one stream).  Allocates nothing. */

@@ -188,6 +188,8 @@ constexpr int kAttnCtasPerSm = 2;  // 2 x 4 consumers x 3 stages x 8.7 KB = 209 
 // Per-stage item header, written by the producer with the first page of an
 // item: {row, head | chunk << 16, len, pages | chunks << 16} (row -1 = the
 // list ended), the query scale at byte 16 and the 64 query bytes at byte 32.
+// Every page also sets the int at byte 24: 1 if its copy was issued, 0 if
+// its page id was outside the pool (the stage then holds stale bytes).
 constexpr int kAttnHdrBytes = 96;
 constexpr int kAttnHdrOffset = kAttnStages * kKvBlockBytes + 256;
 // then the producer's landing slot for the consumer's next work-list record
@@ -286,7 +288,12 @@ __global__ void __launch_bounds__(256) attn_work_kernel(AttnArgs a) {
     const int nc = chunks_of(ri);
     const int items = a.heads * nc;
     AttnItem it;
-    if (nc == 0 && threadIdx.x == 0) attn_item(a, ri * a.heads * a.max_chunks, it);  // records an out-of-range row
+    if (nc == 0) {  // an out-of-range row: no items, status recorded, NaN output
+        if (threadIdx.x == 0) attn_item(a, ri * a.heads * a.max_chunks, it);
+        const int row = a.row_order ? a.row_order[ri] : ri;
+        for (int t = threadIdx.x; t < a.heads * kHeadDim; t += blockDim.x)
+            a.out[(size_t)row * a.heads * kHeadDim + t] = __int_as_float(0x7fc00000);
+    }
     for (int t = threadIdx.x; t < items; t += blockDim.x) {
         const int head = t / nc, chunk = t - head * nc;
         if (attn_item(a, (ri * a.heads + head) * a.max_chunks + chunk, it)) a.work[base + t] = attn_work_of(a, it);
@@ -423,6 +430,7 @@ __device__ __forceinline__ void attn_producer(const AttnArgs &a, uint8_t *smem, 
                     *reinterpret_cast<int4 *>(hdr) = make_int4(cur.row, cur.head_chunk, cur.len, cur.pages_chunks);
                     *reinterpret_cast<float *>(hdr + 16) = qs_cur;
                 }
+                *reinterpret_cast<int *>(hdr + 24) = page_ok ? 1 : 0;  // a skipped page poisons its item
                 if (tx == 0) {
                     mbar_arrive(bar);
                 } else {
@@ -495,6 +503,7 @@ __device__ __forceinline__ void attn_consumer(const AttnArgs &a, uint8_t *smem, 
 #pragma unroll
             for (int i = 0; i < 4; i++) acc_i[mt][i] = 0, acc_f[mt][i] = 0.0f;
         int held = 0;  // pages summed in acc_i since the last flush
+        bool poisoned = false;  // a page of this item was skipped: the item publishes NaN
         const int p0 = 16 * tig + gid, p1 = p0 + 8;
         for (int pg = 0; pg < it.n_pages; pg++) {
             const int stage = consumed % kAttnStages;
@@ -516,6 +525,7 @@ __device__ __forceinline__ void attn_consumer(const AttnArgs &a, uint8_t *smem, 
             }
             const float2 ks = *reinterpret_cast<const float2 *>(blk + kKScaleOffset + 8 * lane);
             const float2 vs = *reinterpret_cast<const float2 *>(blk + kVScaleOffset + 8 * lane);
+            if (!*reinterpret_cast<const int *>(headers + stage * kAttnHdrBytes + 24)) poisoned = true;
             __syncwarp();
             if (lane == 0) mbar_arrive(&e_bar[stage]);
             consumed++;
@@ -596,6 +606,11 @@ __device__ __forceinline__ void attn_consumer(const AttnArgs &a, uint8_t *smem, 
             o[mt][0] = fmaf(t[0], 65536.0f, fmaf(t[1], 256.0f, d2a)) * unscale;
             o[mt][1] = fmaf(t[2], 65536.0f, fmaf(t[3], 256.0f, d2b)) * unscale;
         }
+        if (poisoned) {  // NaN output (or NaN partial, which the merge turns into a NaN output)
+#pragma unroll
+            for (int mt = 0; mt < 4; mt++) o[mt][0] = o[mt][1] = __int_as_float(0x7fc00000);
+            m = l = __int_as_float(0x7fc00000);
+        }
         const size_t rh_index = (size_t)it.row * a.heads + it.head;
         float *out = a.out + rh_index * kHeadDim;
         if (it.n_chunks == 1) {
@@ -665,8 +680,8 @@ __global__ void __launch_bounds__(256) attn_merge_kernel(AttnArgs a) {
     const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (w >= a.rows * a.heads) return;
     const int row = w / a.heads;
-    const int len = a.row_pos[row] + 1;
-    if (len < 1 || len > a.max_pages * kPagePositions) return;
+    const int len = a.row_pos[row] + 1, slot = a.row_slot[row];
+    if (len < 1 || len > a.max_pages * kPagePositions || slot < 0 || slot >= a.slots) return;  // NaN already
     const int pages = (len + kPagePositions - 1) / kPagePositions;
     const int n_chunks = (pages + a.chunk_pages - 1) / a.chunk_pages;
     if (n_chunks < 2) return;
@@ -697,8 +712,8 @@ __global__ void __launch_bounds__(1024) attn_merge_quantize_kernel(AttnArgs a) {
     __shared__ float head_peak[32];
     const int row = blockIdx.x, head = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int w = row * a.heads + head;
-    const int len = a.row_pos[row] + 1;
-    const bool valid = len >= 1 && len <= a.max_pages * kPagePositions;
+    const int len = a.row_pos[row] + 1, slot = a.row_slot[row];
+    const bool valid = len >= 1 && len <= a.max_pages * kPagePositions && slot >= 0 && slot < a.slots;
     const int pages = (len + kPagePositions - 1) / kPagePositions;
     const int n_chunks = valid ? (pages + a.chunk_pages - 1) / a.chunk_pages : 1;
     float2 *o = reinterpret_cast<float2 *>(a.out + (size_t)w * kHeadDim + 2 * lane);
@@ -760,17 +775,15 @@ int launch_attn_decode(const AttnArgs &a, cudaStream_t stream, bool build_work, 
     if (a.chunk_pages < 1 || a.chunk_pages > kAttnMaxChunkPages)
         return set_error(NDL_ERR_INVALID_ARG, "attention: %d pages per item (1..%d)", a.chunk_pages,
                          kAttnMaxChunkPages);
-    static bool configured = false;  // per process; the attribute is per device function
-    static int sms = 0;
-    if (!configured) {
+    static DeviceOnce smem_attribute;  // the attribute belongs to the kernel on one device
+    int st0 = smem_attribute.run([] {
         cudaError_t e = cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              kAttnSmem);
         if (e != cudaSuccess) return set_error(NDL_ERR_CUDA, "attention smem attribute: %s", cudaGetErrorString(e));
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        configured = true;
-    }
+        return (int)NDL_OK;
+    });
+    if (st0 != NDL_OK) return st0;
+    const int sms = device_sm_count();
     const long long items = (long long)a.rows * a.heads * a.max_chunks;
     if (items > 0x7FFFFFFF) return set_error(NDL_ERR_INVALID_ARG, "attention: too many work items");
     if (build_work) {
@@ -873,7 +886,10 @@ extern "C" NDL_API int ndl_attention_paged(const int8_t *q, const float *qs, con
 // ---------------------------------------------------------------------------
 namespace {
 
-constexpr size_t kNoAllocScratchBytes = 4u << 20;  // 4 MiB: 512 rows x 8 heads x 3 chunks (partials + work list) fit
+// 4 MiB: 320 bytes per (row, head, 8-page chunk) item (a 272-byte partial
+// and a 48-byte work record) plus 16 bytes of counters, so at most 13107
+// items; 512 rows x 8 heads x 3 chunks (1536 positions) fit.
+constexpr size_t kNoAllocScratchBytes = 4u << 20;
 constexpr int kNoAllocMaxDevices = 64;
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];

@@ -7,6 +7,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+#include <mutex>
 #include <utility>
 
 #include "../../include/needle_cuda.h"
@@ -32,6 +34,39 @@ int check_launch(const char *what);
     } while (0)
 
 inline bool aligned(const void *p, size_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
+
+// ------------------------------------------------------- per-device set-up --
+// A process may drive several GPUs (one engine per device, host threads per
+// engine), and function attributes and SM counts belong to a device, so
+// one-time set-up is keyed by the current device and guarded for threads.
+constexpr int kMaxDevices = 64;
+
+// SM count of the current device, queried once per device.
+int device_sm_count();
+
+// Runs a set-up step once per device: the first caller on each device runs
+// it under a lock, later callers see the flag.  A failed set-up is retried
+// on the next call.
+class DeviceOnce {
+  public:
+    template <class F>
+    int run(F &&setup) {
+        int dev = 0;
+        cudaError_t e = cudaGetDevice(&dev);
+        if (e != cudaSuccess) return set_error(NDL_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+        if (dev < 0 || dev >= kMaxDevices) return set_error(NDL_ERR_UNSUPPORTED, "device %d out of range", dev);
+        if (done_[dev].load(std::memory_order_acquire)) return NDL_OK;
+        std::lock_guard<std::mutex> lock(mutex_);
+        if (done_[dev].load(std::memory_order_relaxed)) return NDL_OK;
+        int st = setup();
+        if (st == NDL_OK) done_[dev].store(true, std::memory_order_release);
+        return st;
+    }
+
+  private:
+    std::atomic<bool> done_[kMaxDevices] = {};
+    std::mutex mutex_;
+};
 
 // ------------------------------------------------------------------ fp16 --
 // Scalar.HalfToSingle (src/Needle/Scalar.cs:121-128): exact for finite

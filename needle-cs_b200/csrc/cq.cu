@@ -379,19 +379,17 @@ int launch_cq_matmul(const uint8_t *indices, const uint16_t *norms, const uint8_
                      int cols, int bits, const int8_t *values, const float *scales, const float *offsets, int stride,
                      int tokens, float *y, int ldy, int row_start, int row_end, cudaStream_t stream) {
     if (tokens == 0 || row_end <= row_start) return NDL_OK;
-    static int sms = 0;
-    static bool configured = false;
-    if (!configured) {
+    static DeviceOnce smem_attribute;
+    int st0 = smem_attribute.run([] {
         const int max_smem = (int)cq_matmul_smem(kCqMaxCols);
         cudaError_t e = cudaFuncSetAttribute(cq_matmul_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
         if (e == cudaSuccess)
             e = cudaFuncSetAttribute(cq_matmul_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
         if (e != cudaSuccess) return set_error(NDL_ERR_CUDA, "cq matmul smem attribute: %s", cudaGetErrorString(e));
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        configured = true;
-    }
+        return (int)NDL_OK;
+    });
+    if (st0 != NDL_OK) return st0;
+    const int sms = device_sm_count();
     CqBook book;
     memcpy(book.bytes, book_bytes, 16);
     book.byte_scale = byte_scale;

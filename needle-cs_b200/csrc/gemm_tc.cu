@@ -397,26 +397,19 @@ static int make_map(CUtensorMap *map, const void *base, int k, int rows, int dep
     return NDL_OK;
 }
 
-static int tc_sms() {
-    static int sms = 0;
-    if (!sms) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    }
-    return sms;
-}
+static int tc_sms() { return device_sm_count(); }
 
 template <int BT, bool kAccOut, bool kResidual>
 static int launch_bt(const MatmulArgs &a, const TcParams &p, cudaStream_t stream) {
     auto kernel = gemm_i8g32_tc_kernel<BT, kAccOut, kResidual>;
     const size_t smem = sizeof(TcSmem<BT>) + 1024;
-    static bool configured = false;
-    if (!configured) {
+    static DeviceOnce smem_attribute;  // one per instantiation and device
+    int st0 = smem_attribute.run([&] {
         cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return set_error(NDL_ERR_CUDA, "gemm smem attribute: %s", cudaGetErrorString(e));
-        configured = true;
-    }
+        return (int)NDL_OK;
+    });
+    if (st0 != NDL_OK) return st0;
     CUtensorMap map_w, map_x;
     // weights [batch][n][k], activations [1][m][k]: both 3-D, so one load
     // instruction serves either

@@ -355,12 +355,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 5 - kChunks) gemv_i8g32_reg_k
 }
 
 int launch_gemv_i8g32(const MatmulArgs &a, cudaStream_t stream) {
-    static int sms = 0;
-    if (!sms) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    }
+    const int sms = device_sm_count();
     const long long tiles = (long long)((a.n + 7) / 8) * a.batch;
     const long long mtiles = (a.m + 15) / 16;
     if (mtiles > 65535 || tiles + (long long)sms * 5 * kGemvWarps > 0x7fffffffLL)

@@ -24,6 +24,17 @@ int check_launch(const char *what) {
     return NDL_OK;
 }
 
+int device_sm_count() {
+    static std::atomic<int> counts[kMaxDevices];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 1;
+    int n = counts[dev].load(std::memory_order_relaxed);
+    if (n > 0) return n;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n < 1) return 1;
+    counts[dev].store(n, std::memory_order_relaxed);
+    return n;
+}
+
 // ------------------------------------------------------------ generators --
 template <typename F>
 __global__ void synth_fill_kernel(size_t count, F f) {

@@ -52,3 +52,22 @@ def test_paged_attention_flags_bad_rows(ops, cuda):
                         t(case["page_table"]), t(case["pool"]), case["page_bytes"], case["layer"], status=status)
     torch.cuda.synchronize()
     assert status.item() == 2
+
+
+def test_paged_attention_on_a_second_device(ops, oracle, cuda):
+    """One process driving two GPUs: the kernel's shared-memory attribute and
+    the SM count are set up per device, so a call on device 1 after device 0
+    launches with the same result."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two visible GPUs")
+    lengths = [40, 700, 1024]
+    case = make_case(21, lengths, 8)
+    ref = oracle_out(oracle, case, lengths)
+    first = _run(ops, cuda, case)
+    second_dev = torch.device("cuda:1")
+    with torch.cuda.device(second_dev):
+        second = _run(ops, second_dev, case)
+    assert np.array_equal(first, second)
+    for r in range(len(lengths)):
+        peak = np.abs(ref[r]).max()
+        assert np.all(np.abs(second[r] - ref[r]) <= 5e-5 * peak), lengths[r]

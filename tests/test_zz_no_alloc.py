@@ -2,24 +2,27 @@
 
 It serves hosts that must not allocate while handling a request, such as a
 frame-budgeted game or job thread or a zero-allocation serving loop, where a
-cudaMalloc could block or synchronise the device.  Its partials live in a
-fixed device array owned by the library instead of a workspace.
+cudaMalloc could block or synchronise the device.  Its partials and work list
+live in a fixed 4 MiB device array owned by the library instead of a
+workspace.
 
 Checked through the C ABI against the regular entry point
 (ndl_attention_paged) on the same inputs, for two calls in a row (the second
 call reuses the array the first one left dirty), within the attention
-tolerance the other tests use (5e-5 x peak |output|).  Collected last so a
-failure here cannot hide the rest of the suite; it also passes on its own.
+tolerance the other tests use (5e-5 x peak |output|), and against the CPU
+oracle.  The size limit is pinned at its edge.  Collected last so a failure
+here cannot hide the rest of the suite; it also passes on its own.
 """
 import numpy as np
 import pytest
 import torch
 
-from attention_support import make_case
+from attention_support import make_case, oracle_out
 
 pytestmark = pytest.mark.gpu
 
 LENGTHS = [1, 64, 65, 300, 513, 1024, 1088, 7]
+SCRATCH_BYTES = 4 << 20
 
 
 def _args(case, cuda):
@@ -31,49 +34,124 @@ def _args(case, cuda):
 def _call(name, d, case, out, status, extra=()):
     from needle_cs_b200._native import call
 
-    rows, heads = case["q_perm"].shape[:2]
-    slots, max_pages = case["page_table"].shape
+    rows, heads = d["q"].shape[:2]
+    slots, max_pages = d["page_table"].shape
     call(name, d["q"].data_ptr(), d["qs"].data_ptr(), d["row_slot"].data_ptr(), d["row_pos"].data_ptr(), rows,
          heads, d["page_table"].data_ptr(), slots, max_pages, d["pool"].data_ptr(), case["page_bytes"],
          d["pool"].numel() // case["page_bytes"], case["layer"], out.data_ptr(), *extra, status.data_ptr(),
          torch.cuda.current_stream().cuda_stream)
 
 
-def test_noalloc_matches_regular_entry_point_twice(pkg, cuda):
-    case = make_case(29, LENGTHS, 8)
-    d = _args(case, cuda)
-    rows, heads = case["q_perm"].shape[:2]
+def _regular(d, case, cuda):
+    rows, heads = d["q"].shape[:2]
     status = torch.zeros(1, dtype=torch.int32, device=cuda)
     ref = torch.empty((rows, heads, 64), dtype=torch.float32, device=cuda)
     _call("ndl_attention_paged", d, case, ref, status, extra=(None, 0))
     torch.cuda.synchronize()
-    ref = ref.cpu().numpy()
-    for _ in range(2):
-        out = torch.full((rows, heads, 64), float("nan"), dtype=torch.float32, device=cuda)
-        _call("ndl_attention_paged_noalloc", d, case, out, status)
-        torch.cuda.synchronize()
-        got = out.cpu().numpy()
-        assert status.item() == 0
-        for r in range(rows):
-            peak = np.abs(ref[r]).max()
-            assert np.all(np.abs(got[r] - ref[r]) <= 5e-5 * peak), LENGTHS[r]
+    assert status.item() == 0
+    return ref.cpu().numpy()
 
 
-def test_noalloc_rejects_requests_beyond_its_buffer(pkg, cuda):
+def _noalloc(d, case, cuda):
+    rows, heads = d["q"].shape[:2]
+    status = torch.zeros(1, dtype=torch.int32, device=cuda)
+    out = torch.full((rows, heads, 64), 12345.0, dtype=torch.float32, device=cuda)
+    _call("ndl_attention_paged_noalloc", d, case, out, status)
+    torch.cuda.synchronize()
+    return out.cpu().numpy(), status.item()
+
+
+def _close(got, ref):
+    for r in range(ref.shape[0]):
+        peak = np.abs(ref[r]).max()
+        assert np.all(np.abs(got[r] - ref[r]) <= 5e-5 * peak), r
+
+
+def test_noalloc_matches_regular_entry_point_twice(pkg, oracle, cuda):
+    case = make_case(29, LENGTHS, 8)
+    d = _args(case, cuda)
+    ref = _regular(d, case, cuda)
+    _close(ref, oracle_out(oracle, case, LENGTHS))
+    free = []
+    for _ in range(3):
+        got, st = _noalloc(d, case, cuda)
+        assert st == 0
+        _close(got, ref)
+        free.append(torch.cuda.mem_get_info()[0])
+    # after the first call (which may load the library's module on this
+    # device) the calls leave the device's free memory unchanged
+    assert free[1] == free[2]
+
+
+def test_noalloc_bad_page_gives_nan_not_the_last_result(pkg, cuda):
+    """The array keeps the previous call's partials.  A row whose second
+    chunk has a page outside the pool must not merge them: its heads come
+    out NaN with status 2, and the other rows are unaffected."""
+    case = make_case(31, LENGTHS, 8)
+    d = _args(case, cuda)
+    first, st = _noalloc(d, case, cuda)
+    assert st == 0
+    bad_row = LENGTHS.index(1024)  # 16 pages = two 8-page chunks
+    pt = case["page_table"].copy()
+    pt[bad_row, 9] = d["pool"].numel() // case["page_bytes"] + 5
+    d["page_table"] = torch.from_numpy(pt).to(cuda)
+    got, st = _noalloc(d, case, cuda)
+    assert st == 2
+    assert np.all(np.isnan(got[bad_row]))
+    others = [r for r in range(len(LENGTHS)) if r != bad_row]
+    assert np.array_equal(got[others], first[others])
+    # a row with an out-of-range slot is skipped and NaN as well
+    rs = case["row_slot"].copy()
+    rs[0] = 1000
+    d["page_table"] = torch.from_numpy(case["page_table"]).to(cuda)
+    d["row_slot"] = torch.from_numpy(rs).to(cuda)
+    got, st = _noalloc(d, case, cuda)
+    assert st == 2
+    assert np.all(np.isnan(got[0]))
+    assert np.array_equal(got[1:], first[1:])
+
+
+def _max_items(ops, heads, max_pages):
+    """Largest row count whose workspace fits the 4 MiB array."""
+    lo, hi = 1, 1 << 20
+    while lo < hi:
+        mid = (lo + hi + 1) // 2
+        if ops.attention_paged_workspace(mid, heads, max_pages) <= SCRATCH_BYTES:
+            lo = mid
+        else:
+            hi = mid - 1
+    return lo
+
+
+def test_noalloc_limit_at_its_edge(pkg, ops, cuda):
+    """Each (row, head, chunk) item takes a 272-byte partial and a 48-byte
+    work record (320 bytes), so 4 MiB holds 13107 one-head, one-chunk rows:
+    13107 run and equal the regular entry point, 13108 are refused on the
+    host before any device work."""
     from needle_cs_b200 import NeedleError
 
-    case = make_case(3, [10, 20], 8)
+    rows = _max_items(ops, 1, 1)
+    assert rows == 13107
+    assert ops.attention_paged_workspace(rows, 1, 1) <= SCRATCH_BYTES < ops.attention_paged_workspace(rows + 1, 1, 1)
+    base = make_case(7, [1, 9, 33, 64, 17, 50, 2, 63], 1, max_pages=1)
+    n = len(base["row_slot"])
+    idx = np.arange(rows) % n
+    case = dict(base, q_perm=base["q_perm"][idx], QS=base["QS"][idx], row_slot=base["row_slot"][idx],
+                row_pos=base["row_pos"][idx])
     d = _args(case, cuda)
+    ref = _regular(d, case, cuda)
+    got, st = _noalloc(d, case, cuda)
+    assert st == 0
+    assert np.array_equal(got, ref)
+    over = np.arange(rows + 1) % n
+    case_over = dict(base, q_perm=base["q_perm"][over], QS=base["QS"][over], row_slot=base["row_slot"][over],
+                     row_pos=base["row_pos"][over])
+    d_over = _args(case_over, cuda)
     status = torch.zeros(1, dtype=torch.int32, device=cuda)
-    out = torch.empty((2, 8, 64), dtype=torch.float32, device=cuda)
-    from needle_cs_b200._native import call
-
-    # 4 MiB holds at most 15420 (row, head, chunk) partials of 272 bytes; the
-    # request is refused on the host before any device memory is touched
+    out = torch.empty((rows + 1, 1, 64), dtype=torch.float32, device=cuda)
     with pytest.raises(NeedleError) as e:
-        call("ndl_attention_paged_noalloc", d["q"].data_ptr(), d["qs"].data_ptr(), d["row_slot"].data_ptr(),
-             d["row_pos"].data_ptr(), 4096, 8, d["page_table"].data_ptr(), 2, 17, d["pool"].data_ptr(),
-             case["page_bytes"], d["pool"].numel() // case["page_bytes"], case["layer"], out.data_ptr(),
-             status.data_ptr(), torch.cuda.current_stream().cuda_stream)
+        _call("ndl_attention_paged_noalloc", d_over, case_over, out, status)
     assert e.value.status == 100
     assert "scratch" in str(e.value)
+    torch.cuda.synchronize()
+    assert status.item() == 0
