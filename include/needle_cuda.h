@@ -147,24 +147,29 @@ NDL_API int ndl_matmul_i8g32_batched(const int8_t *q, const float *sa, int m, co
 
 /* Paged int8 decode attention: the device-pointer counterpart of the
  * AttentionTile / AttentionBatch kernel slots (Scalar.AttentionHead
- * src/Needle/Scalar.cs:290-312, AttentionBatch + MergePartials
- * src/Needle/Blocks.cs:750-990).  For row r and head h it attends to
- * positions 0..row_pos[r] of slot row_slot[r]:
- *   s_j = (q . k_j) * ks_j * (qs[r][h] / 8);  p = softmax(s);  out = sum_j p_j vs_j v_j
+ * src/Needle/Scalar.cs:290-312, AttentionBatch src/Needle/Blocks.cs:830-990).
+ * For row r and head h it attends to positions 0..row_pos[r] of slot
+ * row_slot[r], with every rounding of Scalar.AttentionHead in its order:
+ *   s_j = ((q . k_j) * ks_j) * (qs[r][h] / 8);  e_j = exp(s_j - max s);
+ *   total = e_0 + e_1 + ... (in position order);  p_j = e_j / total;
+ *   out = 0;  out += (p_j * vs_j) * v_j  for j = 0, 1, ...
+ * (exp is the correctly rounded single-precision exponential), so the
+ * output equals the scalar routine's bit for bit.
  * Page layout: a page holds 64 positions of one slot for every layer; the
- * (layer, head) record at ((layer*heads + head) * 8704) is
- *   [K int8 64x64][K scale f32 x64][V^T int8 64x64][V scale f32 x64]
- * K (row = position p, col = dim d) and V^T (row = d, col = pv_col(p)) are
- * stored in mma m16n8k32 A-fragment order: element (row, col) at byte
+ * (layer, head) record at ((layer*heads + head) * 8704) is two halves,
+ *   [K int8 64x64][K scale f32 x64] [V scale f32 x64][V int8 64x64]
+ * K (row = position p, col = dim d) is stored in mma m16n8k32 A-fragment
+ * order: element (row, col) at byte
  *   (row>>4)*1024 + (col>>5)*512 + ((row&7)*4 + (col>>2&3))*16
  *   + ((row>>3&1) + 2*(col>>4&1))*4 + (col&3)
- * with pv_col(p) = 32*(g>>2) + 16*(g>>1&1) + 4*(p>>4&3) + 2*(g&1) + (p>>3&1),
- * g = p&7; the scales of p sit at index 2*((p&7)*4 + (p>>4&3)) + (p>>3&1).
+ * and the K scale of p at index 2*((p&7)*4 + (p>>4&3)) + (p>>3&1).  The V
+ * scales are in position order; V (p, d) sits at byte 4608 +
+ * d*64 + ((((p>>4) ^ ((d>>1)&3)) << 4) | (p&15)) of the record.
  * The query's dims are in the order k_slot(d) = ((d&15)>>2)*16 + (d>>4)*4 + (d&3).
  * q: int8 [rows][heads][64] in k_slot order; qs [rows][heads]; out fp32
- * [rows][heads][64].  Rows longer than 512 positions are split into
- * 512-position chunks merged afterwards; the chunk partials live in
- * `workspace` (NULL: allocated and freed on `stream` by the library).
+ * [rows][heads][64]; max_pages * 64 <= 8192.  The work list (one record per
+ * row) lives in `workspace` (NULL: allocated and freed on `stream` by the
+ * library).
  * status (nullable, device int) receives 2 for an out-of-range slot, page
  * or length and 1 for a timed-out wait.  A row with an out-of-range slot or
  * length, and a head whose pages include one outside the pool, is skipped
@@ -180,12 +185,13 @@ NDL_API int ndl_attention_paged(const int8_t *q, const float *qs, const int32_t 
  * (frame-budgeted game or job threads, audio callbacks, zero-allocation
  * request loops), where cudaMalloc could block or synchronise the device.
  * Same arguments and results as ndl_attention_paged, without a workspace:
- * the chunk partials and the work list live in a 4 MiB device array owned
- * by the library (held on every GPU that loads it until exit).  Requests
- * whose ndl_attention_paged_workspace(rows, heads, max_pages) exceeds 4 MiB
- * are rejected with NDL_ERR_INVALID_ARG: each (row, head, 512-position
- * chunk) takes 320 bytes, so rows * heads * ceil(max_pages / 8) may be at
- * most 13107 (512 rows x 8 heads x 3 chunks = 1536 positions fit).  The first call on a device looks the array up
+ * the work list lives in a 4 MiB device array owned by the library (held
+ * on every GPU that loads it until exit).  Requests whose
+ * ndl_attention_paged_workspace(rows, heads, max_pages) exceeds 4 MiB are
+ * rejected with NDL_ERR_INVALID_ARG: each row takes 16 + 4 * max_pages
+ * bytes (max_pages rounded up to a multiple of 4), so rows *
+ * (16 + 4 * max_pages) + 16 may be at most 4 MiB; 512 rows fit at any
+ * supported max_pages (<= 128).  The first call on a device looks the array up
  * (cudaGetSymbolAddress) and must come before any stream capture.  All
  * calls share the array: calls that overlap on the GPU race and must be
  * ordered by the caller (e.g. one stream).  Allocates nothing. */

@@ -1,23 +1,24 @@
-// Paged int8 KV cache: the KV-write epilogue and split-K decode attention.
+// Paged int8 KV cache: the KV-write epilogue and decode attention.
 //
 // KV write (src/Needle/Engine.cs:2552-2569): RoPE at the row's absolute
 // position (half-split rotation, Scalar.Rope src/Needle/Scalar.cs:233-248),
 // then QuantizeInt8 of q per head and of k, v per (position, head) into the
 // slot's page.  Bit-exact: round-to-nearest products, no FMA.
 //
-// Decode attention (Scalar.AttentionHead src/Needle/Scalar.cs:290-312,
-// AttentionBatch.ExecuteChunk + MergePartials src/Needle/Blocks.cs:750-990):
-// persistent warps stream (row, head, chunk of pages) items from a work list
-// built once per step.  Each page's 8704-byte (layer, head) record arrives
-// in shared memory by one cp.async.bulk, issued by a producer warp into a
-// 3-stage ring per consumer warp (mbarrier completion, bounded waits).
-// Scores are exact int8 dots (mma.sync s8) scaled by ks * (qs / sqrt(d));
-// softmax is online (running max, rescaled sum) in fp32 with expf; V is
-// accumulated exactly by mma.sync s8 x u8 over 24-bit fixed-point
-// probability weights.  A row longer than one chunk (a fixed number of
-// pages, so the split depends only on the row's own length) writes (peak,
-// sum, unnormalised output) partials that attn_merge_kernel combines with
-// exp(peak - max) weights, like MergePartials.
+// Decode attention, bit for bit Scalar.AttentionHead (src/Needle/Scalar.cs:
+// 290-312) over the whole row: persistent warps stream (row, head) items from
+// a work list built once per step.  Each page's (layer, head) record arrives
+// in shared memory as two bulk copies (K half, V half), issued by a producer
+// warp into a ring per consumer warp (mbarrier completion, bounded waits).
+// Pass A: the int8 dots on tensor cores (mma.sync s8, exact int32), then
+// (dot * ks) * (qs / sqrt(d)) per position into a shared score buffer.
+// Softmax in the reference's order: max, exp(s - max) per position, their
+// total summed in position order by one lane, each divided by it.  Pass B:
+// out[d] += (p * vs) * v[d] in position order, two dims per lane on packed
+// f32x2 instructions.  Every rounding is the reference's, so the output is
+// the scalar result exactly (the exponential is the correctly rounded one,
+// exp_rn).  The merge of split partials (MergePartials,
+// src/Needle/Blocks.cs:750-817) is not needed: a row is never split.
 #include <mutex>
 
 #include "common.cuh"
@@ -93,7 +94,7 @@ __global__ void __launch_bounds__(256) kv_write_kernel(KvWriteArgs a) {
         if (ok) {
             blk[k_byte(j, lane)] = (uint8_t)lo8;
             blk[k_byte(j, lane + 32)] = (uint8_t)hi8;
-            if (lane == 0) reinterpret_cast<float *>(blk + kKScaleOffset)[scale_slot(j)] = scale;
+            if (lane == 0) reinterpret_cast<float *>(blk + kKScaleOffset)[k_scale_index(j)] = scale;
         }
     }
     // v: per-(position, head) quantize into the page
@@ -103,7 +104,7 @@ __global__ void __launch_bounds__(256) kv_write_kernel(KvWriteArgs a) {
         if (ok) {
             blk[v_byte(j, lane)] = (uint8_t)lo8;
             blk[v_byte(j, lane + 32)] = (uint8_t)hi8;
-            if (lane == 0) reinterpret_cast<float *>(blk + kVScaleOffset)[scale_slot(j)] = scale;
+            if (lane == 0) reinterpret_cast<float *>(blk + kVScaleOffset)[v_scale_index(j)] = scale;
         }
     }
 }
@@ -164,11 +165,11 @@ __global__ void __launch_bounds__(256) cross_kv_write_kernel(const float *__rest
     float scale = warp_quantize64(kr[lane], kr[lane + 32], lo8, hi8);
     blk[k_byte(j, lane)] = (uint8_t)lo8;
     blk[k_byte(j, lane + 32)] = (uint8_t)hi8;
-    if (lane == 0) reinterpret_cast<float *>(blk + kKScaleOffset)[scale_slot(j)] = scale;
+    if (lane == 0) reinterpret_cast<float *>(blk + kKScaleOffset)[k_scale_index(j)] = scale;
     scale = warp_quantize64(vr[lane], vr[lane + 32], lo8, hi8);
     blk[v_byte(j, lane)] = (uint8_t)lo8;
     blk[v_byte(j, lane + 32)] = (uint8_t)hi8;
-    if (lane == 0) reinterpret_cast<float *>(blk + kVScaleOffset)[scale_slot(j)] = scale;
+    if (lane == 0) reinterpret_cast<float *>(blk + kVScaleOffset)[v_scale_index(j)] = scale;
 }
 
 int launch_cross_kv_write(const float *y, int frames, int heads, const int32_t *page_row, int num_pages, uint8_t *pool,
@@ -182,56 +183,38 @@ int launch_cross_kv_write(const float *y, int frames, int heads, const int32_t *
 
 // ------------------------------------------------------ decode attention --
 constexpr int kAttnConsumers = 4;  // consumer warps per CTA; warp 4 is the producer
-constexpr int kAttnStages = 3;     // ring stages per consumer
+constexpr int kAttnStages = 4;     // ring stages (half records) per consumer
 constexpr int kAttnThreads = 32 * (kAttnConsumers + 1);
-constexpr int kAttnCtasPerSm = 2;  // 2 x 4 consumers x 3 stages x 8.7 KB = 209 KB of ring per SM
-// Per-stage item header, written by the producer with the first page of an
-// item: {row, head | chunk << 16, len, pages | chunks << 16} (row -1 = the
-// list ended), the query scale at byte 16 and the 64 query bytes at byte 32.
-// Every page also sets the int at byte 24: 1 if its copy was issued, 0 if
-// its page id was outside the pool (the stage then holds stale bytes).
+// Per-stage header, written by the producer: with an item's first copy
+// {row, head, len, pages} (row -1 = the list ended), the query scale at byte
+// 16 and the 64 query bytes at byte 32; with every copy the int at byte 24:
+// 1 if the page was copied, 0 if its id was outside the pool (the stage then
+// holds stale bytes and the item's output becomes NaN).
 constexpr int kAttnHdrBytes = 96;
-constexpr int kAttnHdrOffset = kAttnStages * kKvBlockBytes + 256;
-// then the producer's landing slot for the consumer's next work-list record
-constexpr int kAttnEntryOffset = kAttnHdrOffset + kAttnStages * kAttnHdrBytes;
-constexpr int kConsumerSmem = kAttnEntryOffset + (int)sizeof(AttnWork);  // ring, digits, headers, record
-static_assert(kConsumerSmem % 16 == 0 && kAttnEntryOffset % 16 == 0, "bulk copy destinations");
-constexpr int kAttnBarOffset = kAttnConsumers * kConsumerSmem;  // full[c][s], empty[c][s], record[c]
-constexpr int kAttnSmem = kAttnBarOffset + (2 * kAttnConsumers * kAttnStages + kAttnConsumers) * 8;
 // A producer lane reads the result of its item claim (an atomic) and of a
 // query-scale load only this many SM cycles after issuing them, so the
 // warp's other lanes are not held on the load's scoreboard.
 constexpr long long kAttnLatencyCycles = 1000;
-// int32 PV accumulators gain at most 64 * 255 * 128 per page; flushing to
-// fp32 every 1024 pages keeps them below 2^31.
-constexpr int kHoldPages = 1024;
 constexpr uint32_t kWaitLimit = 1u << 22;
 constexpr uint32_t kPollLimit = 1u << 24;  // producer polls without progress (with a short sleep each)
 
-// Work item i = (row in LPT order, head, chunk) with chunk innermost.
-struct AttnItem {
-    int row, head, chunk, n_chunks, first_page, n_pages, len, slot;
+// Shared memory of one CTA for rows of at most max_pages pages: per consumer
+// [ring stages][stage headers][64 PV weights][2 work records][scores], then
+// the barriers full[consumer][stage], empty[consumer][stage], record[consumer].
+struct AttnSmem {
+    int record_bytes, hdr, wbuf, rec, scores, consumer, bars, total;
 };
-
-__device__ __forceinline__ bool attn_item(const AttnArgs &a, int i, AttnItem &it) {
-    const int chunk = i % a.max_chunks;
-    const int rh = i / a.max_chunks;
-    it.head = rh % a.heads;
-    const int ri = rh / a.heads;
-    it.row = a.row_order ? a.row_order[ri] : ri;
-    it.len = a.row_pos[it.row] + 1;
-    it.slot = a.row_slot[it.row];
-    if (it.len < 1 || it.len > a.max_pages * kPagePositions || it.slot < 0 || it.slot >= a.slots) {
-        if (a.status) atomicOr(a.status, kStatusBadPage);  // out-of-range row: skipped
-        return false;
-    }
-    const int pages = (it.len + kPagePositions - 1) / kPagePositions;
-    it.n_chunks = (pages + a.chunk_pages - 1) / a.chunk_pages;
-    if (chunk >= it.n_chunks) return false;
-    it.chunk = chunk;
-    it.first_page = chunk * a.chunk_pages;
-    it.n_pages = min(pages, it.first_page + a.chunk_pages) - it.first_page;
-    return true;
+__host__ __device__ __forceinline__ AttnSmem attn_smem(int max_pages) {
+    AttnSmem s;
+    s.record_bytes = attn_record_ints(max_pages) * 4;
+    s.hdr = kAttnStages * kKvHalfBytes;
+    s.wbuf = s.hdr + kAttnStages * kAttnHdrBytes;
+    s.rec = s.wbuf + kPagePositions * 4;
+    s.scores = s.rec + 2 * s.record_bytes;
+    s.consumer = s.scores + max_pages * kPagePositions * 4;
+    s.bars = kAttnConsumers * s.consumer;
+    s.total = s.bars + (2 * kAttnStages + 1) * kAttnConsumers * 8;
+    return s;
 }
 
 __device__ __forceinline__ void mma_s8s8_m16n8k32(int (&d)[4], const uint4 &a, uint32_t b0, uint32_t b1) {
@@ -241,127 +224,65 @@ __device__ __forceinline__ void mma_s8s8_m16n8k32(int (&d)[4], const uint4 &a, u
         : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
         : "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w), "r"(b0), "r"(b1));
 }
-__device__ __forceinline__ void mma_s8u8_m16n8k32(int (&d)[4], const uint4 &a, uint32_t b0, uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k32.row.col.s32.s8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%0,%1,%2,%3};\n"
-        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
-        : "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w), "r"(b0), "r"(b1));
-}
 
-__device__ __forceinline__ AttnWork attn_work_of(const AttnArgs &a, const AttnItem &it) {
-    AttnWork w;
-    w.row = it.row;
-    w.head_chunk = it.head | (it.chunk << 16);
-    w.len = it.len;
-    w.pages_chunks = it.n_pages | (it.n_chunks << 16);
-#pragma unroll
-    for (int k = 0; k < kAttnMaxChunkPages; k++)
-        w.page[k] = k < it.n_pages ? a.page_table[(size_t)it.slot * a.max_pages + it.first_page + k] : -1;
-    return w;
-}
-
-// The compacted work list: CTA per row position ri of the LPT order.  Its
-// items (head, chunk innermost) start after the items of rows 0..ri-1, so
-// the CTA first sums those rows' chunk counts, then writes its own items
-// with their page ids.
-__global__ void __launch_bounds__(256) attn_work_kernel(AttnArgs a) {
+// The work list: CTA per row position ri of the launch's row order.  An
+// out-of-range row (length or slot) gets zero pages, its status bit and NaN
+// outputs.  CTA 0 sets the item count and clears the kernel's counters.
+__global__ void __launch_bounds__(128) attn_work_kernel(AttnArgs a) {
     pdl_enter();
-    __shared__ int warp_sum[8];
     const int ri = blockIdx.x;
-    auto chunks_of = [&](int r) -> int {  // 0 for an out-of-range row
-        const int row = a.row_order ? a.row_order[r] : r;
-        const int len = a.row_pos[row] + 1, slot = a.row_slot[row];
-        if (len < 1 || len > a.max_pages * kPagePositions || slot < 0 || slot >= a.slots) return 0;
-        const int pages = (len + kPagePositions - 1) / kPagePositions;
-        return (pages + a.chunk_pages - 1) / a.chunk_pages;
-    };
-    int part = 0;
-    for (int r = threadIdx.x; r < ri; r += blockDim.x) part += chunks_of(r);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
-    if ((threadIdx.x & 31) == 0) warp_sum[threadIdx.x >> 5] = part;
-    __syncthreads();
-    int before = 0;
-    for (int w = 0; w < (int)(blockDim.x >> 5); w++) before += warp_sum[w];
-    const int base = a.heads * before;
-    const int nc = chunks_of(ri);
-    const int items = a.heads * nc;
-    AttnItem it;
-    if (nc == 0) {  // an out-of-range row: no items, status recorded, NaN output
-        if (threadIdx.x == 0) attn_item(a, ri * a.heads * a.max_chunks, it);
-        const int row = a.row_order ? a.row_order[ri] : ri;
+    int32_t *rec = a.work + (size_t)ri * attn_record_ints(a.max_pages);
+    const int row = a.row_order ? a.row_order[ri] : ri;
+    const int len = a.row_pos[row] + 1, slot = a.row_slot[row];
+    const bool valid = len >= 1 && len <= a.max_pages * kPagePositions && slot >= 0 && slot < a.slots;
+    const int pages = valid ? (len + kPagePositions - 1) / kPagePositions : 0;
+    if (threadIdx.x == 0) {
+        *reinterpret_cast<int4 *>(rec) = make_int4(row, len, slot, pages);
+        if (!valid && a.status) atomicOr(a.status, kStatusBadPage);
+        if (ri == 0) {
+            a.n_work[0] = a.rows * a.heads;
+            a.n_work[1] = 0;
+            a.n_work[2] = 0;
+        }
+    }
+    for (int t = threadIdx.x; t < pages; t += blockDim.x)
+        rec[4 + t] = a.page_table[(size_t)slot * a.max_pages + t];
+    if (!valid)
         for (int t = threadIdx.x; t < a.heads * kHeadDim; t += blockDim.x)
             a.out[(size_t)row * a.heads * kHeadDim + t] = __int_as_float(0x7fc00000);
-    }
-    for (int t = threadIdx.x; t < items; t += blockDim.x) {
-        const int head = t / nc, chunk = t - head * nc;
-        if (attn_item(a, (ri * a.heads + head) * a.max_chunks + chunk, it)) a.work[base + t] = attn_work_of(a, it);
-    }
-    if (ri == a.rows - 1 && threadIdx.x == 0) {
-        a.n_work[0] = base + items;
-        a.n_work[1] = 0;  // the decode kernel's item counter and finish count
-        a.n_work[2] = 0;
-    }
 }
 
-// Persistent, warp-specialised.  The work list (rows sorted longest first,
-// heads and chunks of a row adjacent) is dealt dynamically: consumer warp w
-// takes item w first (its record and query scale loaded directly, as nothing
-// is in flight yet to hide them behind); after that, whenever its producer lane starts
-// issuing an item it claims the next unclaimed one from a counter in global
-// memory.  Warps that stream slower (the rate differs by SM and over time)
-// so take fewer items and the launch's warps finish together; claiming one
-// item ahead keeps the claims in step with progress.
-// Lane c of the producer warp feeds consumer c of its CTA.  It runs a small
-// state machine per lane so that no lane's latency holds the warp: claim
-// (atomic; its result read kAttnLatencyCycles later), fetch the item's
-// 48-byte record into shared memory (cp.async.bulk, completion polled on
-// its own mbarrier), load the query scale (read kAttnLatencyCycles later).
-// It issues the consumer's page copies (one cp.async.bulk per 8704-byte
-// page record) into the consumer's 3-stage ring as stages free up; with an
-// item's first page it writes the item header (metadata, query scale) into
-// the stage and copies the 64 query bytes beside it, so a consumer never
-// loads metadata from global memory.
-// A consumer waits for a page, moves its K and V^T fragments and scales to
-// registers, frees the stage and computes, all products on int8 tensor cores:
-//  * QK: mma.sync m16n8k32 s8, A = K (16 positions x 32 dims), B = the
-//    query in every column: exact int32 dots.  Lane (gid, tig) keeps tile
-//    tig, i.e. positions 16*tig + gid and 16*tig + gid + 8.
-//  * PV: the weights w' = p * vs * 2^e (e keeps w' below 2^12, folded into
-//    the online-softmax rescale) become 24-bit fixed point W = w' * 2^12,
-//    split into three unsigned byte digits.  mma.sync m16n8k32 s8 x u8 with
-//    A = V^T (16 dims x 32 positions) and B = the digits (column = digit)
-//    gives exact int32 sums of digit x v, chained across pages in the
-//    accumulator until the softmax rescale changes; the digits recombine
-//    as D0 * 2^16 + D1 * 2^8 + D2 once per item.
-// Every wait and the producer's polling are bounded.  The last CTA to finish
-// returns the counters to zero for the next launch on the same list.
-__device__ __forceinline__ void attn_producer(const AttnArgs &a, uint8_t *smem, uint64_t *full, uint64_t *empty,
-                                              uint64_t *record_bar, int lane) {
+// Persistent, warp-specialised.  Items are (row position, head) with heads
+// innermost, rows longest first; consumer warp w takes item w first, after
+// that its producer lane claims the next unclaimed item from a counter in
+// global memory whenever it starts issuing the current one, so warps that
+// stream slower take fewer items and the launch's warps finish together.
+// Lane c of the producer warp feeds consumer c through a small state machine
+// so that no lane's latency holds the warp: claim (atomic; read
+// kAttnLatencyCycles later), fetch the item's row record with its page ids
+// into shared memory (cp.async.bulk, double-buffered, polled on its own
+// mbarrier), load the query scale (read kAttnLatencyCycles later).  Per item
+// it issues 2 * pages copies into the consumer's ring: every page's K half,
+// then every page's V half; with the first it writes the item header and
+// copies the 64 query bytes beside it.  Every wait and poll is bounded.
+__device__ __forceinline__ void attn_producer(const AttnArgs &a, const AttnSmem &L, uint8_t *smem, uint64_t *full,
+                                              uint64_t *empty, uint64_t *record_bar, int lane) {
     const int W = gridDim.x * kAttnConsumers;
     const int c = lane;
     const int n_work = a.n_work[0];
     int *next_item = a.n_work + 1;
+    const int rec_ints = L.record_bytes / 4;
     enum { kClaimed, kFetching, kScale, kReady, kExhausted };
     bool done = c >= kAttnConsumers, ending = false;
-    uint8_t *record = smem + c * kConsumerSmem + kAttnEntryOffset;
-    AttnWork cur{}, nx{};
-    float qs_cur = 0.0f, qs_nx = 0.0f;
+    uint8_t *base = smem + (size_t)(done ? 0 : c) * L.consumer;
     int fs = kClaimed, claim = blockIdx.x * kAttnConsumers + c;  // the first item is this warp's own
+    int nx_buf = 0, cur_buf = 1;
+    int nx_row = 0, nx_head = 0, nx_len = 0, nx_pages = 0;
+    int cur_row = 0, cur_head = 0, cur_len = 0, cur_pages = 0;
+    float qs_nx = 0.0f, qs_cur = 0.0f;
     long long t_issue = clock64() - kAttnLatencyCycles;
-    unsigned fetches = 0;
-    if (!done) {  // the first record and scale load directly: nothing is in flight yet to hide them behind
-        if (claim < n_work) {
-            nx = a.work[claim];
-            qs_nx = __ldg(a.qs + (size_t)nx.row * a.heads + (nx.head_chunk & 0xFFFF));
-            fs = kReady;
-        } else {
-            fs = kExhausted;
-        }
-    }
-    int k = 0, n_pages = 0;
-    unsigned issued = 0;
+    unsigned fetches = 0, issued = 0;
+    int k = 0;  // next copy of the current item: K halves 0..pages-1, then V halves
     uint32_t idle = 0;
     bool timed_out = false;
     while (true) {
@@ -371,29 +292,39 @@ __device__ __forceinline__ void attn_producer(const AttnArgs &a, uint8_t *smem, 
             // one step of the next item's fetch
             if (fs == kClaimed && clock64() - t_issue >= kAttnLatencyCycles) {
                 if (claim < n_work) {
-                    uint64_t *bar = &record_bar[c];
+                    nx_head = claim % a.heads;
                     fence_proxy_async_smem();
-                    mbar_arrive_expect_tx(bar, (uint32_t)sizeof(AttnWork));
-                    bulk_g2s(record, a.work + claim, (uint32_t)sizeof(AttnWork), bar);
+                    mbar_arrive_expect_tx(&record_bar[c], (uint32_t)L.record_bytes);
+                    bulk_g2s(base + L.rec + nx_buf * L.record_bytes, a.work + (size_t)(claim / a.heads) * rec_ints,
+                             (uint32_t)L.record_bytes, &record_bar[c]);
                     fs = kFetching;
                 } else {
                     fs = kExhausted;
                 }
             } else if (fs == kFetching && mbar_test_wait(&record_bar[c], fetches & 1)) {
                 fetches++;
-                nx = *reinterpret_cast<const AttnWork *>(record);
-                qs_nx = __ldg(a.qs + (size_t)nx.row * a.heads + (nx.head_chunk & 0xFFFF));
+                const int4 h = *reinterpret_cast<const int4 *>(base + L.rec + nx_buf * L.record_bytes);
+                nx_row = h.x;
+                nx_len = h.y;
+                nx_pages = h.w;
                 t_issue = clock64();
-                fs = kScale;
+                if (nx_pages == 0) {  // an out-of-range row: nothing to attend, take another item
+                    claim = W + atomicAdd(next_item, 1);
+                    fs = kClaimed;
+                } else {
+                    qs_nx = __ldg(a.qs + (size_t)nx_row * a.heads + nx_head);
+                    fs = kScale;
+                }
             } else if (fs == kScale && clock64() - t_issue >= kAttnLatencyCycles) {
                 fs = kReady;
             }
             // the next item starts once the current one is issued
-            if (!ending && k == n_pages) {
+            if (!ending && k == 2 * cur_pages) {
                 if (fs == kReady) {
-                    cur = nx;
+                    cur_row = nx_row, cur_head = nx_head, cur_len = nx_len, cur_pages = nx_pages;
                     qs_cur = qs_nx;
-                    n_pages = cur.pages_chunks & 0xFFFF;
+                    cur_buf = nx_buf;
+                    nx_buf ^= 1;
                     k = 0;
                     claim = W + atomicAdd(next_item, 1);
                     t_issue = clock64();
@@ -402,7 +333,7 @@ __device__ __forceinline__ void attn_producer(const AttnArgs &a, uint8_t *smem, 
                     ending = true;
                 }
             }
-            if (ending || k < n_pages) {
+            if (ending || k < 2 * cur_pages) {
                 stage = issued % kAttnStages;
                 send = issued < (unsigned)kAttnStages ||
                        mbar_test_wait(&empty[c * kAttnStages + stage], ((issued / kAttnStages) - 1) & 1);
@@ -410,37 +341,37 @@ __device__ __forceinline__ void attn_producer(const AttnArgs &a, uint8_t *smem, 
         }
         if (send) {  // lanes with a free stage issue together
             uint64_t *bar = &full[c * kAttnStages + stage];
-            uint8_t *hdr = smem + c * kConsumerSmem + kAttnHdrOffset + stage * kAttnHdrBytes;
+            uint8_t *hdr = base + L.hdr + stage * kAttnHdrBytes;
             if (ending) {  // end marker: no copy, the consumer reads row -1 and stops
                 *reinterpret_cast<int4 *>(hdr) = make_int4(-1, 0, 0, 0);
                 mbar_arrive(bar);
                 done = true;
             } else {
                 const bool first = k == 0;
-                int page = -1;
-#pragma unroll
-                for (int j = 0; j < kAttnMaxChunkPages; j++)
-                    if (j == k) page = cur.page[j];
+                const bool v_half = k >= cur_pages;
+                const int pi = v_half ? k - cur_pages : k;
+                const int page = reinterpret_cast<const int *>(base + L.rec + cur_buf * L.record_bytes)[4 + pi];
                 k++;
                 const bool page_ok = page >= 0 && page < a.num_pages;
                 if (!page_ok && a.status) atomicOr(a.status, kStatusBadPage);
-                const uint32_t tx = (page_ok ? kKvBlockBytes : 0) + (first ? kHeadDim : 0);
-                const int head = cur.head_chunk & 0xFFFF;
                 if (first) {
-                    *reinterpret_cast<int4 *>(hdr) = make_int4(cur.row, cur.head_chunk, cur.len, cur.pages_chunks);
+                    *reinterpret_cast<int4 *>(hdr) = make_int4(cur_row, cur_head, cur_len, cur_pages);
                     *reinterpret_cast<float *>(hdr + 16) = qs_cur;
                 }
-                *reinterpret_cast<int *>(hdr + 24) = page_ok ? 1 : 0;  // a skipped page poisons its item
+                *reinterpret_cast<int *>(hdr + 24) = page_ok ? 1 : 0;
+                const uint32_t tx = (page_ok ? kKvHalfBytes : 0) + (first ? kHeadDim : 0);
                 if (tx == 0) {
                     mbar_arrive(bar);
                 } else {
                     fence_proxy_async_smem();
                     mbar_arrive_expect_tx(bar, tx);
                     if (page_ok)
-                        bulk_g2s(smem + c * kConsumerSmem + stage * kKvBlockBytes,
-                                 a.pool + (size_t)page * a.page_bytes + kv_block_offset(a.layer, head, a.heads),
-                                 kKvBlockBytes, bar);
-                    if (first) bulk_g2s(hdr + 32, a.q + ((size_t)cur.row * a.heads + head) * kHeadDim, kHeadDim, bar);
+                        bulk_g2s(base + stage * kKvHalfBytes,
+                                 a.pool + (size_t)page * a.page_bytes + kv_block_offset(a.layer, cur_head, a.heads) +
+                                     (v_half ? kKvHalfBytes : 0),
+                                 kKvHalfBytes, bar);
+                    if (first)
+                        bulk_g2s(hdr + 32, a.q + ((size_t)cur_row * a.heads + cur_head) * kHeadDim, kHeadDim, bar);
                 }
             }
             issued++;
@@ -458,20 +389,61 @@ __device__ __forceinline__ void attn_producer(const AttnArgs &a, uint8_t *smem, 
     }
     if (timed_out && lane == 0 && a.status) atomicOr(a.status, kStatusTimeout);
     // drain: every copy this lane issued lands before the CTA exits (bounded)
-    if (fs == kFetching) mbar_wait_bounded(&record_bar[c], fetches & 1, kWaitLimit);
-    for (unsigned j = issued > (unsigned)kAttnStages ? issued - kAttnStages : 0u; j < issued; j++)
-        mbar_wait_bounded(&full[c * kAttnStages + j % kAttnStages], (j / kAttnStages) & 1, kWaitLimit);
+    if (c < kAttnConsumers) {
+        if (fs == kFetching) mbar_wait_bounded(&record_bar[c], fetches & 1, kWaitLimit);
+        for (unsigned j = issued > (unsigned)kAttnStages ? issued - kAttnStages : 0u; j < issued; j++)
+            mbar_wait_bounded(&full[c * kAttnStages + j % kAttnStages], (j / kAttnStages) & 1, kWaitLimit);
+    }
 }
 
-__device__ __forceinline__ void attn_consumer(const AttnArgs &a, uint8_t *smem, uint64_t *full, uint64_t *empty,
-                                              int warp, int lane) {
+// Sum of s[0..n) in position order (one lane: the reference's loop).
+__device__ __forceinline__ float sum_in_order(const float *s, int n) {
+    float t = 0.0f;
+    int j = 0;
+    for (; j + 4 <= n; j += 4) {
+        const float4 v = *reinterpret_cast<const float4 *>(s + j);
+        t = __fadd_rn(t, v.x);
+        t = __fadd_rn(t, v.y);
+        t = __fadd_rn(t, v.z);
+        t = __fadd_rn(t, v.w);
+    }
+    for (; j < n; j++) t = __fadd_rn(t, s[j]);
+    return t;
+}
+
+// One 16-position chunk of pass B for the lane's two dims: va / vb hold the
+// chunk's V bytes of dim lane and lane + 32, w the chunk's 16 weights.
+// Each int8 becomes an exact float through its biased byte (v ^ 0x80 as the
+// low mantissa byte of 2^23), then acc += w * v per position in order.
+__device__ __forceinline__ uint64_t pv_chunk(uint64_t acc, const uint4 &va, const uint4 &vb, const float *w) {
+    const uint32_t wa[4] = {va.x ^ 0x80808080u, va.y ^ 0x80808080u, va.z ^ 0x80808080u, va.w ^ 0x80808080u};
+    const uint32_t wb[4] = {vb.x ^ 0x80808080u, vb.y ^ 0x80808080u, vb.z ^ 0x80808080u, vb.w ^ 0x80808080u};
+    const uint64_t bias = f2_pack(-8388736.0f, -8388736.0f);  // -(2^23 + 128)
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+        const float4 w4 = *reinterpret_cast<const float4 *>(w + 4 * q);
+        const float ww[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const float fa = __uint_as_float(__byte_perm(wa[q], 0x4B000000u, 0x7540u + i));
+            const float fb = __uint_as_float(__byte_perm(wb[q], 0x4B000000u, 0x7540u + i));
+            const uint64_t v = f2_add(f2_pack(fa, fb), bias);  // exact: both are integers below 2^24
+            acc = f2_add(acc, f2_mul(f2_pack(ww[i], ww[i]), v));
+        }
+    }
+    return acc;
+}
+
+__device__ __forceinline__ void attn_consumer(const AttnArgs &a, const AttnSmem &L, uint8_t *smem, uint64_t *full,
+                                              uint64_t *empty, int warp, int lane) {
     const int gid = lane >> 2, tig = lane & 3;
-    uint8_t *ring = smem + warp * kConsumerSmem;
-    uint8_t *digits = ring + kAttnStages * kKvBlockBytes;  // [digit 0..2, unused zero row][tig][16 bytes]
-    const uint8_t *headers = ring + kAttnHdrOffset;
+    uint8_t *base = smem + (size_t)warp * L.consumer;
+    const uint8_t *headers = base + L.hdr;
+    float *wbuf = reinterpret_cast<float *>(base + L.wbuf);
+    float *sc = reinterpret_cast<float *>(base + L.scores);
     uint64_t *f_bar = full + warp * kAttnStages, *e_bar = empty + warp * kAttnStages;
-    reinterpret_cast<uint2 *>(digits)[lane] = make_uint2(0u, 0u);
-    __syncwarp();
+    const int p0 = 16 * tig + gid, p1 = p0 + 8;  // the positions of this lane's two QK results
+    const int swz = (lane >> 1) & 3;             // V chunk rotation of dims lane and lane + 32
     unsigned consumed = 0;
     bool timed_out = false;
     while (!timed_out) {
@@ -486,50 +458,28 @@ __device__ __forceinline__ void attn_consumer(const AttnArgs &a, uint8_t *smem, 
         if (meta.x < 0) break;  // the list ended for this warp
         const uint4 qv = *reinterpret_cast<const uint4 *>(hdr + 32 + tig * 16);  // K-dim chunk tig, both k-steps
         const float scale = __fmul_rn(*reinterpret_cast<const float *>(hdr + 16), a.inv_sqrt_d);
-        AttnItem it;
-        it.row = meta.x;
-        it.head = meta.y & 0xFFFF;
-        it.chunk = meta.y >> 16;
-        it.len = meta.z;
-        it.n_pages = meta.w & 0xFFFF;
-        it.n_chunks = meta.w >> 16;
-        it.first_page = it.chunk * a.chunk_pages;
-        float m = -INFINITY, l = 0.0f;
-        int e_acc = 12;  // power-of-two scale currently applied to the accumulators
-        int acc_i[4][4];
-        float acc_f[4][4];
-#pragma unroll
-        for (int mt = 0; mt < 4; mt++)
-#pragma unroll
-            for (int i = 0; i < 4; i++) acc_i[mt][i] = 0, acc_f[mt][i] = 0.0f;
-        int held = 0;  // pages summed in acc_i since the last flush
-        bool poisoned = false;  // a page of this item was skipped: the item publishes NaN
-        const int p0 = 16 * tig + gid, p1 = p0 + 8;
-        for (int pg = 0; pg < it.n_pages; pg++) {
+        const int row = meta.x, head = meta.y, len = meta.z, n_pages = meta.w;
+        bool poisoned = false;
+        float peak = -INFINITY;
+        // ---- pass A: s_j = (dot_j * ks_j) * scale for every position ----
+        for (int pg = 0; pg < n_pages; pg++) {
             const int stage = consumed % kAttnStages;
             if (pg > 0 && !mbar_wait_bounded(&f_bar[stage], (consumed / kAttnStages) & 1, kWaitLimit)) {
                 timed_out = true;
                 break;
             }
-            const uint8_t *blk = ring + stage * kKvBlockBytes;
-            const int valid = min(kPagePositions, it.len - (it.first_page + pg) * kPagePositions);
-            // the page into registers (K and V^T fragments, scales); then the
-            // stage goes back to the producer while this warp computes
-            uint4 kf[4][2], vf[4][2];
+            const uint8_t *blk = base + stage * kKvHalfBytes;
+            uint4 kf[4][2];
 #pragma unroll
             for (int mt = 0; mt < 4; mt++) {
                 kf[mt][0] = *reinterpret_cast<const uint4 *>(blk + mt * 1024 + lane * 16);
                 kf[mt][1] = *reinterpret_cast<const uint4 *>(blk + mt * 1024 + 512 + lane * 16);
-                vf[mt][0] = *reinterpret_cast<const uint4 *>(blk + kVOffset + mt * 1024 + lane * 16);
-                vf[mt][1] = *reinterpret_cast<const uint4 *>(blk + kVOffset + mt * 1024 + 512 + lane * 16);
             }
             const float2 ks = *reinterpret_cast<const float2 *>(blk + kKScaleOffset + 8 * lane);
-            const float2 vs = *reinterpret_cast<const float2 *>(blk + kVScaleOffset + 8 * lane);
             if (!*reinterpret_cast<const int *>(headers + stage * kAttnHdrBytes + 24)) poisoned = true;
             __syncwarp();
             if (lane == 0) mbar_arrive(&e_bar[stage]);
             consumed++;
-            // ---- QK ----
             int dot0 = 0, dot1 = 0;
 #pragma unroll
             for (int mt = 0; mt < 4; mt++) {
@@ -538,112 +488,72 @@ __device__ __forceinline__ void attn_consumer(const AttnArgs &a, uint8_t *smem, 
                 mma_s8s8_m16n8k32(d, kf[mt][1], qv.z, qv.w);
                 if (mt == tig) dot0 = d[0], dot1 = d[2];
             }
-            const float s0 = p0 < valid ? __fmul_rn(__fmul_rn(__int2float_rn(dot0), ks.x), scale) : -INFINITY;
-            const float s1 = p1 < valid ? __fmul_rn(__fmul_rn(__int2float_rn(dot1), ks.y), scale) : -INFINITY;
-            // one combined warp reduction: the page's score max and V-scale max
-            float smax = fmaxf(s0, s1);
-            float vmax = fmaxf(p0 < valid ? vs.x : 0.0f, p1 < valid ? vs.y : 0.0f);
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-                smax = fmaxf(smax, __shfl_xor_sync(0xffffffffu, smax, o));
-                vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, o));
+            const int valid = min(kPagePositions, len - pg * kPagePositions);
+            if (p0 < valid) {
+                const float s0 = __fmul_rn(__fmul_rn(__int2float_rn(dot0), ks.x), scale);
+                sc[pg * kPagePositions + p0] = s0;
+                peak = fmaxf(peak, s0);
             }
-            const float m_new = fmaxf(m, smax);
-            const float e0 = p0 < valid ? expf(s0 - m_new) : 0.0f;
-            const float e1 = p1 < valid ? expf(s1 - m_new) : 0.0f;
-            const float corr = expf(m - m_new);
-            l = l * corr + (e0 + e1);  // this lane's share; reduced across the warp per item
-            m = m_new;
-            // power-of-two range guard: w' = p * vs * 2^e < 2^12 (p <= 1)
-            int ex;
-            frexpf(vmax, &ex);
-            const int e_page = 12 - max(0, ex);
-            const float rescale = corr * exp2f((float)(e_page - e_acc));
-            e_acc = e_page;
-            const float f = exp2f((float)(e_page + 12));
-            // W = w' * 2^12 < 2^24 (an exact power-of-two scaling of w')
-            const uint32_t W0 = p0 < valid ? __float2uint_rn(e0 * vs.x * f) : 0u;
-            const uint32_t W1 = p1 < valid ? __float2uint_rn(e1 * vs.y * f) : 0u;
-            // digits of this lane's two positions, at PV columns pv_col(p0) and pv_col(p0) + 1
-            uint8_t *dg = digits + tig * 16 + 2 * gid;
-            *reinterpret_cast<uint16_t *>(dg) = (uint16_t)__byte_perm(W0, W1, 0x0062);
-            *reinterpret_cast<uint16_t *>(dg + 64) = (uint16_t)__byte_perm(W0, W1, 0x0051);
-            *reinterpret_cast<uint16_t *>(dg + 128) = (uint16_t)__byte_perm(W0, W1, 0x0040);
-            if (rescale != 1.0f || held == kHoldPages) {
-#pragma unroll
-                for (int mt = 0; mt < 4; mt++)
-#pragma unroll
-                    for (int i = 0; i < 4; i++) {
-                        acc_f[mt][i] = (acc_f[mt][i] + __int2float_rn(acc_i[mt][i])) * rescale;
-                        acc_i[mt][i] = 0;
-                    }
-                held = 0;
+            if (p1 < valid) {
+                const float s1 = __fmul_rn(__fmul_rn(__int2float_rn(dot1), ks.y), scale);
+                sc[pg * kPagePositions + p1] = s1;
+                peak = fmaxf(peak, s1);
             }
-            held++;
-            __syncwarp();
-            // ---- PV: column n of B is digit n & 3 (digit 3 = the zero row) ----
-            const uint4 b = *reinterpret_cast<const uint4 *>(digits + (gid & 3) * 64 + tig * 16);
-#pragma unroll
-            for (int mt = 0; mt < 4; mt++) {
-                mma_s8u8_m16n8k32(acc_i[mt], vf[mt][0], b.x, b.y);
-                mma_s8u8_m16n8k32(acc_i[mt], vf[mt][1], b.z, b.w);
-            }
-            __syncwarp();  // the digits are read before the next page rewrites them
         }
         if (timed_out) break;
-        l = warp_sum_f(l);
-        // lane (gid, 0) holds digits 0 and 1 of dims 16*mt + gid (+8), lane
-        // (gid, 1) digit 2: o = (D0 * 2^16 + D1 * 2^8 + D2) * 2^-(12 + e)
-        const float unscale = exp2f((float)(-12 - e_acc));
-        float o[4][2];
-#pragma unroll
-        for (int mt = 0; mt < 4; mt++) {
-            float t[4];
-#pragma unroll
-            for (int i = 0; i < 4; i++) t[i] = acc_f[mt][i] + __int2float_rn(acc_i[mt][i]);
-            const float d2a = __shfl_down_sync(0xffffffffu, t[0], 1);
-            const float d2b = __shfl_down_sync(0xffffffffu, t[2], 1);
-            o[mt][0] = fmaf(t[0], 65536.0f, fmaf(t[1], 256.0f, d2a)) * unscale;
-            o[mt][1] = fmaf(t[2], 65536.0f, fmaf(t[3], 256.0f, d2b)) * unscale;
-        }
-        if (poisoned) {  // NaN output (or NaN partial, which the merge turns into a NaN output)
-#pragma unroll
-            for (int mt = 0; mt < 4; mt++) o[mt][0] = o[mt][1] = __int_as_float(0x7fc00000);
-            m = l = __int_as_float(0x7fc00000);
-        }
-        const size_t rh_index = (size_t)it.row * a.heads + it.head;
-        float *out = a.out + rh_index * kHeadDim;
-        if (it.n_chunks == 1) {
-            const float inv = 1.0f / l;
-            if (tig == 0)
-#pragma unroll
-                for (int mt = 0; mt < 4; mt++) {
-                    out[16 * mt + gid] = o[mt][0] * inv;
-                    out[16 * mt + gid + 8] = o[mt][1] * inv;
-                }
-            continue;
-        }
-        // long row: publish this chunk's (unnormalised output, peak, sum);
-        // attn_merge_kernel combines them after this launch
-        float *part = a.partials + (rh_index * a.max_chunks + it.chunk) * kPartialFloats;
-        if (tig == 0)
-#pragma unroll
-            for (int mt = 0; mt < 4; mt++) {
-                part[16 * mt + gid] = o[mt][0];
-                part[16 * mt + gid + 8] = o[mt][1];
+        // ---- softmax (Scalar.Softmax): exp(s - peak), total in position order, p = e / total ----
+        peak = warp_max_f(peak);
+        __syncwarp();
+        for (int j = lane; j < len; j += 32) sc[j] = exp_rn(__fsub_rn(sc[j], peak));
+        __syncwarp();
+        float total = lane == 0 ? sum_in_order(sc, len) : 0.0f;
+        total = __shfl_sync(0xffffffffu, total, 0);
+        for (int j = lane; j < len; j += 32) sc[j] = __fdiv_rn(sc[j], total);
+        __syncwarp();
+        // ---- pass B: out[d] += (p_j * vs_j) * v_j[d] in position order ----
+        uint64_t acc = f2_pack(0.0f, 0.0f);  // dims lane, lane + 32
+        for (int pg = 0; pg < n_pages; pg++) {
+            const int stage = consumed % kAttnStages;
+            if (!mbar_wait_bounded(&f_bar[stage], (consumed / kAttnStages) & 1, kWaitLimit)) {
+                timed_out = true;
+                break;
             }
-        if (lane == 0) {
-            part[64] = m;
-            part[65] = l;
+            const uint8_t *blk = base + stage * kKvHalfBytes;  // [V scales][V dim-major]
+            const float *vs = reinterpret_cast<const float *>(blk);
+            const int valid = min(kPagePositions, len - pg * kPagePositions);
+            // positions past the row's end get weight 0: 0 * v adds a zero, which leaves acc unchanged
+            wbuf[lane] = lane < valid ? __fmul_rn(sc[pg * kPagePositions + lane], vs[lane]) : 0.0f;
+            wbuf[lane + 32] = lane + 32 < valid ? __fmul_rn(sc[pg * kPagePositions + lane + 32], vs[lane + 32]) : 0.0f;
+            uint4 va[4], vb[4];
+#pragma unroll
+            for (int ch = 0; ch < 4; ch++) {
+                va[ch] = *reinterpret_cast<const uint4 *>(blk + 256 + lane * 64 + ((ch ^ swz) << 4));
+                vb[ch] = *reinterpret_cast<const uint4 *>(blk + 256 + (lane + 32) * 64 + ((ch ^ swz) << 4));
+            }
+            if (!*reinterpret_cast<const int *>(headers + stage * kAttnHdrBytes + 24)) poisoned = true;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&e_bar[stage]);
+            consumed++;
+#pragma unroll
+            for (int ch = 0; ch < 4; ch++) acc = pv_chunk(acc, va[ch], vb[ch], wbuf + 16 * ch);
+            __syncwarp();  // the weights are read before the next page rewrites them
         }
+        if (timed_out) break;
+        float o0, o1;
+        f2_unpack(acc, o0, o1);
+        if (poisoned) o0 = o1 = __int_as_float(0x7fc00000);
+        float *out = a.out + ((size_t)row * a.heads + head) * kHeadDim;
+        out[lane] = o0;
+        out[lane + 32] = o1;
     }
     if (timed_out && lane == 0 && a.status) atomicOr(a.status, kStatusTimeout);
 }
 
-__global__ void __launch_bounds__(kAttnThreads, kAttnCtasPerSm) attn_decode_kernel(AttnArgs a) {
+__global__ void __launch_bounds__(kAttnThreads, 2) attn_decode_kernel(AttnArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
+    const AttnSmem L = attn_smem(a.max_pages);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem + kAttnBarOffset);  // [consumer][stage]
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + L.bars);  // [consumer][stage]
     uint64_t *empty = full + kAttnConsumers * kAttnStages;
     uint64_t *record_bar = empty + kAttnConsumers * kAttnStages;  // [consumer]
     if (threadIdx.x == 0) {
@@ -655,9 +565,9 @@ __global__ void __launch_bounds__(kAttnThreads, kAttnCtasPerSm) attn_decode_kern
     pdl_wait();
     pdl_trigger();
     if (warp == kAttnConsumers)
-        attn_producer(a, smem, full, empty, record_bar, lane);
+        attn_producer(a, L, smem, full, empty, record_bar, lane);
     else
-        attn_consumer(a, smem, full, empty, warp, lane);
+        attn_consumer(a, L, smem, full, empty, warp, lane);
     // every producer lane has taken its last item: the last CTA out resets
     // the item counter and the finish count for the next launch
     __syncthreads();
@@ -671,72 +581,15 @@ __global__ void __launch_bounds__(kAttnThreads, kAttnCtasPerSm) attn_decode_kern
     }
 }
 
-// Combines the chunks of every long row (Attention.MergePartials,
-// src/Needle/Blocks.cs:750-817): out = sum_c w_c o_c / sum_c w_c l_c with
-// w_c = exp(peak_c - max peak), chunks in ascending order.  Warp per
-// (row, head); lane owns dims 2*lane, 2*lane+1.
-__global__ void __launch_bounds__(256) attn_merge_kernel(AttnArgs a) {
-    pdl_enter();
-    const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-    if (w >= a.rows * a.heads) return;
-    const int row = w / a.heads;
-    const int len = a.row_pos[row] + 1, slot = a.row_slot[row];
-    if (len < 1 || len > a.max_pages * kPagePositions || slot < 0 || slot >= a.slots) return;  // NaN already
-    const int pages = (len + kPagePositions - 1) / kPagePositions;
-    const int n_chunks = (pages + a.chunk_pages - 1) / a.chunk_pages;
-    if (n_chunks < 2) return;
-    const float *parts = a.partials + (size_t)w * a.max_chunks * kPartialFloats;
-    float peak = -INFINITY;
-    for (int c = 0; c < n_chunks; c++) peak = fmaxf(peak, parts[c * kPartialFloats + 64]);
-    float total = 0.0f, m0 = 0.0f, m1 = 0.0f;
-    for (int c = 0; c < n_chunks; c++) {
-        const float *pc = parts + c * kPartialFloats;
-        const float wgt = expf(pc[64] - peak);
-        total += wgt * pc[65];
-        const float2 v = *reinterpret_cast<const float2 *>(pc + 2 * lane);
-        m0 += wgt * v.x;
-        m1 += wgt * v.y;
-    }
-    const float inv = 1.0f / total;
-    *reinterpret_cast<float2 *>(a.out + (size_t)w * kHeadDim + 2 * lane) = make_float2(m0 * inv, m1 * inv);
-}
-
-// attn_merge_kernel fused with the per-row quantize of the attention
-// output (the o-projection's input), bit-identical to the two launches:
-// CTA per row, warp per head; a head of a one-chunk row is read back from
-// out.  The row peak (exact max of |x| over heads x 64) goes through shared
-// memory; scale, inverse and rounding as Scalar.QuantizeInt8
-// (src/Needle/Scalar.cs:67-74).
-__global__ void __launch_bounds__(1024) attn_merge_quantize_kernel(AttnArgs a) {
+// The per-row quantize of the attention output (the o-projection's input):
+// CTA per row, warp per head; the row peak (exact max of |x| over heads x 64)
+// goes through shared memory; scale, inverse and rounding as
+// Scalar.QuantizeInt8 (src/Needle/Scalar.cs:67-74).
+__global__ void __launch_bounds__(1024) attn_quantize_kernel(AttnArgs a) {
     pdl_enter();
     __shared__ float head_peak[32];
     const int row = blockIdx.x, head = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int w = row * a.heads + head;
-    const int len = a.row_pos[row] + 1, slot = a.row_slot[row];
-    const bool valid = len >= 1 && len <= a.max_pages * kPagePositions && slot >= 0 && slot < a.slots;
-    const int pages = (len + kPagePositions - 1) / kPagePositions;
-    const int n_chunks = valid ? (pages + a.chunk_pages - 1) / a.chunk_pages : 1;
-    float2 *o = reinterpret_cast<float2 *>(a.out + (size_t)w * kHeadDim + 2 * lane);
-    float2 v;
-    if (n_chunks >= 2) {
-        const float *parts = a.partials + (size_t)w * a.max_chunks * kPartialFloats;
-        float peak = -INFINITY;
-        for (int c = 0; c < n_chunks; c++) peak = fmaxf(peak, parts[c * kPartialFloats + 64]);
-        float total = 0.0f, m0 = 0.0f, m1 = 0.0f;
-        for (int c = 0; c < n_chunks; c++) {
-            const float *pc = parts + c * kPartialFloats;
-            const float wgt = expf(pc[64] - peak);
-            total += wgt * pc[65];
-            const float2 pv = *reinterpret_cast<const float2 *>(pc + 2 * lane);
-            m0 += wgt * pv.x;
-            m1 += wgt * pv.y;
-        }
-        const float inv = 1.0f / total;
-        v = make_float2(m0 * inv, m1 * inv);
-        *o = v;
-    } else {
-        v = *o;
-    }
+    const float2 v = *reinterpret_cast<const float2 *>(a.out + ((size_t)row * a.heads + head) * kHeadDim + 2 * lane);
     const float hp = warp_max_f(fmaxf(fabsf(v.x), fabsf(v.y)));
     if (lane == 0) head_peak[head] = hp;
     __syncthreads();
@@ -753,87 +606,93 @@ __global__ void __launch_bounds__(1024) attn_merge_quantize_kernel(AttnArgs a) {
 int launch_attn_work(const AttnArgs &a, cudaStream_t stream) {
     if (a.rows == 0) return NDL_OK;
     if (!a.work || !a.n_work) return set_error(NDL_ERR_INVALID_ARG, "attention: no work list");
-    launch_kernel(attn_work_kernel, dim3(a.rows), dim3(256), 0, stream, a);
+    launch_kernel(attn_work_kernel, dim3(a.rows), dim3(128), 0, stream, a);
     return check_launch("attn_work");
 }
 
-int launch_attn_merge(const AttnArgs &a, cudaStream_t stream) {
-    if (a.rows == 0) return NDL_OK;
-    if (a.q_out) {
-        if (a.heads > 32) return set_error(NDL_ERR_INVALID_ARG, "attention: %d heads > 32", a.heads);
-        launch_kernel(attn_merge_quantize_kernel, dim3(a.rows), dim3(a.heads * 32), 0, stream, a);
-        return check_launch("attn_merge_quantize");
-    }
-    if (a.max_chunks < 2) return NDL_OK;
-    const int warps = a.rows * a.heads;
-    launch_kernel(attn_merge_kernel, dim3((warps + 7) / 8), dim3(256), 0, stream, a);
-    return check_launch("attn_merge");
+int launch_attn_quantize(const AttnArgs &a, cudaStream_t stream) {
+    if (a.rows == 0 || !a.q_out) return NDL_OK;
+    if (a.heads > 32) return set_error(NDL_ERR_INVALID_ARG, "attention: %d heads > 32", a.heads);
+    launch_kernel(attn_quantize_kernel, dim3(a.rows), dim3(a.heads * 32), 0, stream, a);
+    return check_launch("attn_quantize");
 }
 
-int launch_attn_decode(const AttnArgs &a, cudaStream_t stream, bool build_work, bool merge) {
+// CTAs of attn_decode_kernel that fit one SM at this shared-memory size,
+// cached per device and size.
+static int attn_ctas_per_sm(size_t smem) {
+    struct Entry {
+        int dev;
+        size_t smem;
+        int ctas;
+    };
+    static std::mutex mutex;
+    static Entry cache[32];
+    static int used = 0;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 1;
+    std::lock_guard<std::mutex> lock(mutex);
+    for (int i = 0; i < used; i++)
+        if (cache[i].dev == dev && cache[i].smem == smem) return cache[i].ctas;
+    int ctas = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&ctas, attn_decode_kernel, kAttnThreads, smem) != cudaSuccess ||
+        ctas < 1)
+        ctas = 1;
+    if (used < 32) cache[used++] = Entry{dev, smem, ctas};
+    return ctas;
+}
+
+int launch_attn_decode(const AttnArgs &a, cudaStream_t stream, bool build_work, bool quantize) {
     if (a.rows == 0) return NDL_OK;
-    if (a.chunk_pages < 1 || a.chunk_pages > kAttnMaxChunkPages)
-        return set_error(NDL_ERR_INVALID_ARG, "attention: %d pages per item (1..%d)", a.chunk_pages,
-                         kAttnMaxChunkPages);
+    if (a.max_pages < 1 || a.max_pages * kPagePositions > kAttnMaxPositions)
+        return set_error(NDL_ERR_UNSUPPORTED, "attention: %d pages per row (at most %d positions)", a.max_pages,
+                         kAttnMaxPositions);
     static DeviceOnce smem_attribute;  // the attribute belongs to the kernel on one device
     int st0 = smem_attribute.run([] {
-        cudaError_t e = cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             kAttnSmem);
+        int dev = 0, optin = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+        cudaError_t e = cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, optin);
         if (e != cudaSuccess) return set_error(NDL_ERR_CUDA, "attention smem attribute: %s", cudaGetErrorString(e));
         return (int)NDL_OK;
     });
     if (st0 != NDL_OK) return st0;
-    const int sms = device_sm_count();
-    const long long items = (long long)a.rows * a.heads * a.max_chunks;
+    const size_t smem = (size_t)attn_smem(a.max_pages).total;
+    const long long items = (long long)a.rows * a.heads;
     if (items > 0x7FFFFFFF) return set_error(NDL_ERR_INVALID_ARG, "attention: too many work items");
     if (build_work) {
         int st = launch_attn_work(a, stream);
         if (st != NDL_OK) return st;
     }
     long long blocks = (items + kAttnConsumers - 1) / kAttnConsumers;
-    const long long resident = (long long)sms * kAttnCtasPerSm;  // the CTAs that fit the shared memory
+    const long long resident = (long long)device_sm_count() * attn_ctas_per_sm(smem);
     if (blocks > resident) blocks = resident;
-    launch_kernel(attn_decode_kernel, dim3((unsigned)blocks), dim3(kAttnThreads), kAttnSmem, stream, a);
+    launch_kernel(attn_decode_kernel, dim3((unsigned)blocks), dim3(kAttnThreads), smem, stream, a);
     int st = check_launch("attn_decode");
-    if (st != NDL_OK || !merge) return st;
-    return launch_attn_merge(a, stream);
+    if (st != NDL_OK || !quantize) return st;
+    return launch_attn_quantize(a, stream);
 }
 
 }  // namespace ndl
 
 using namespace ndl;
 
-static constexpr int kAbiChunkPages = 8;
-
-// Workspace: the chunk partials [rows][heads][chunks][kPartialFloats] fp32,
-// then the work list [rows * heads * chunks] and 16 bytes for its length and
-// the decode kernel's two counters.
-static size_t abi_partial_bytes(int rows, int heads, int max_pages) {
-    const size_t chunks = (size_t)(max_pages + kAbiChunkPages - 1) / kAbiChunkPages;
-    return ((size_t)rows * heads * chunks * kPartialFloats * sizeof(float) + 15) / 16 * 16;
-}
-
+// Workspace: the work list [rows][attn_record_ints(max_pages)] int32 and 16
+// bytes for the item count and the decode kernel's two counters.
 extern "C" NDL_API size_t ndl_attention_paged_workspace(int rows, int heads, int max_pages) {
     if (rows <= 0 || heads <= 0 || max_pages <= 0) return 0;
-    const size_t chunks = (size_t)(max_pages + kAbiChunkPages - 1) / kAbiChunkPages;
-    return abi_partial_bytes(rows, heads, max_pages) + (size_t)rows * heads * chunks * sizeof(AttnWork) + 16;
+    return (size_t)rows * attn_record_ints(max_pages) * sizeof(int32_t) + 16;
 }
 
-// Points a.partials, a.work and a.n_work into a workspace of that layout.
-static void abi_carve(AttnArgs &a, void *ws, int rows, int heads, int max_pages) {
+// Points a.work and a.n_work into a workspace of that layout.
+static void abi_carve(AttnArgs &a, void *ws, int rows, int max_pages) {
     uint8_t *base = static_cast<uint8_t *>(ws);
-    const size_t pb = abi_partial_bytes(rows, heads, max_pages);
-    const size_t chunks = (size_t)(max_pages + kAbiChunkPages - 1) / kAbiChunkPages;
-    a.partials = reinterpret_cast<float *>(base);
-    a.work = reinterpret_cast<AttnWork *>(base + pb);
-    a.n_work = reinterpret_cast<int *>(base + pb + (size_t)rows * heads * chunks * sizeof(AttnWork));
+    a.work = reinterpret_cast<int32_t *>(base);
+    a.n_work = reinterpret_cast<int *>(base + (size_t)rows * attn_record_ints(max_pages) * sizeof(int32_t));
 }
 
-extern "C" NDL_API int ndl_attention_paged(const int8_t *q, const float *qs, const int32_t *row_slot,
-                                           const int32_t *row_pos, int rows, int heads, const int32_t *page_table,
-                                           int slots, int max_pages, const uint8_t *pool, size_t page_bytes,
-                                           int num_pages, int layer, float *out, void *workspace,
-                                           size_t workspace_bytes, int *status, void *stream) {
+static int abi_check(const int8_t *q, const float *qs, const int32_t *row_slot, const int32_t *row_pos, int rows,
+                     int heads, const int32_t *page_table, int slots, int max_pages, const uint8_t *pool,
+                     size_t page_bytes, int num_pages, int layer, float *out) {
     NDL_REQUIRE(rows >= 0 && heads >= 1 && slots >= 1 && max_pages >= 1 && num_pages >= 1 && layer >= 0,
                 "bad attention geometry");
     if (rows == 0) return NDL_OK;
@@ -841,6 +700,20 @@ extern "C" NDL_API int ndl_attention_paged(const int8_t *q, const float *qs, con
     NDL_REQUIRE(page_bytes % 16 == 0 && page_bytes >= kv_block_offset(layer, heads - 1, heads) + kKvBlockBytes,
                 "page_bytes %zu cannot hold layer %d of %d heads", page_bytes, layer, heads);
     NDL_REQUIRE(aligned(q, 16) && aligned(pool, 16) && aligned(out, 16) && aligned(qs, 4), "misaligned pointer");
+    if ((long long)max_pages * kPagePositions > kAttnMaxPositions)
+        return set_error(NDL_ERR_UNSUPPORTED, "attention: %d pages per row; at most %d positions", max_pages,
+                         kAttnMaxPositions);
+    return NDL_OK;
+}
+
+extern "C" NDL_API int ndl_attention_paged(const int8_t *q, const float *qs, const int32_t *row_slot,
+                                           const int32_t *row_pos, int rows, int heads, const int32_t *page_table,
+                                           int slots, int max_pages, const uint8_t *pool, size_t page_bytes,
+                                           int num_pages, int layer, float *out, void *workspace,
+                                           size_t workspace_bytes, int *status, void *stream) {
+    int rc = abi_check(q, qs, row_slot, row_pos, rows, heads, page_table, slots, max_pages, pool, page_bytes,
+                       num_pages, layer, out);
+    if (rc != NDL_OK || rows == 0) return rc;
     const size_t need = ndl_attention_paged_workspace(rows, heads, max_pages);
     cudaStream_t st = (cudaStream_t)stream;
     void *ws = workspace;
@@ -851,10 +724,9 @@ extern "C" NDL_API int ndl_attention_paged(const int8_t *q, const float *qs, con
         NDL_CUDA(cudaMallocAsync(&ws, need, st));
     }
     AttnArgs a{q, qs, row_slot, row_pos, nullptr, page_table, max_pages, pool, (long long)page_bytes, num_pages,
-               layer, heads, rows, kAbiChunkPages, (max_pages + kAbiChunkPages - 1) / kAbiChunkPages,
-               0.125f, out, nullptr, nullptr, status, slots};
-    abi_carve(a, ws, rows, heads, max_pages);
-    int rc = launch_attn_decode(a, st);
+               layer, heads, rows, 0.125f, out, status, slots, nullptr, nullptr, nullptr, nullptr};
+    abi_carve(a, ws, rows, max_pages);
+    rc = launch_attn_decode(a, st);
     if (!workspace) cudaFreeAsync(ws, st);
     return rc;
 }
@@ -868,8 +740,8 @@ extern "C" NDL_API int ndl_attention_paged(const int8_t *q, const float *qs, con
 // allocations.  cudaMalloc can block for a long time, serialises on a
 // driver-wide lock and can synchronise the device, so such callers cannot
 // supply the workspace ndl_attention_paged needs, nor let it allocate one.
-// This entry point keeps the chunk partials in a fixed device array that
-// the library owns instead.
+// This entry point keeps the work list (and the kernel's counters) in a
+// fixed device array that the library owns instead.
 //
 // The array is a file-scope __device__ variable, so every GPU that loads
 // this library holds its kNoAllocScratchBytes until the process exits.  On
@@ -879,16 +751,17 @@ extern "C" NDL_API int ndl_attention_paged(const int8_t *q, const float *qs, con
 // Make that first call before any stream capture starts.
 //
 // Every call shares the one array.  Nothing in it has to start at zero: a
-// launch writes each chunk partial before the merge reads it.  Two calls
-// whose work overlaps on the GPU (different streams, or no ordering between
-// them) race on the array and can corrupt each other's results; callers
-// must order them, for example by issuing them on one stream.
+// launch's first kernel writes every work record and clears the counters
+// before the attention kernel reads them.  Two calls whose work overlaps on
+// the GPU (different streams, or no ordering between them) race on the
+// array and can corrupt each other's results; callers must order them, for
+// example by issuing them on one stream.
 // ---------------------------------------------------------------------------
 namespace {
 
-// 4 MiB: 320 bytes per (row, head, 8-page chunk) item (a 272-byte partial
-// and a 48-byte work record) plus 16 bytes of counters, so at most 13107
-// items; 512 rows x 8 heads x 3 chunks (1536 positions) fit.
+// 4 MiB: a work record of 16 bytes plus 4 per page-table column (rounded up
+// to 16) per row, plus 16 bytes of counters; 512 rows fit at any supported
+// page-table width (at most 128 pages).
 constexpr size_t kNoAllocScratchBytes = 4u << 20;
 constexpr int kNoAllocMaxDevices = 64;
 
@@ -922,24 +795,19 @@ extern "C" NDL_API int ndl_attention_paged_noalloc(const int8_t *q, const float 
                                                    const int32_t *page_table, int slots, int max_pages,
                                                    const uint8_t *pool, size_t page_bytes, int num_pages, int layer,
                                                    float *out, int *status, void *stream) {
-    NDL_REQUIRE(rows >= 0 && heads >= 1 && slots >= 1 && max_pages >= 1 && num_pages >= 1 && layer >= 0,
-                "bad attention geometry");
-    if (rows == 0) return NDL_OK;
-    NDL_REQUIRE(q && qs && row_slot && row_pos && page_table && pool && out, "null pointer");
-    NDL_REQUIRE(page_bytes % 16 == 0 && page_bytes >= kv_block_offset(layer, heads - 1, heads) + kKvBlockBytes,
-                "page_bytes %zu cannot hold layer %d of %d heads", page_bytes, layer, heads);
-    NDL_REQUIRE(aligned(q, 16) && aligned(pool, 16) && aligned(out, 16) && aligned(qs, 4), "misaligned pointer");
+    int rc = abi_check(q, qs, row_slot, row_pos, rows, heads, page_table, slots, max_pages, pool, page_bytes,
+                       num_pages, layer, out);
+    if (rc != NDL_OK || rows == 0) return rc;
     const size_t need = ndl_attention_paged_workspace(rows, heads, max_pages);
     if (need > kNoAllocScratchBytes)
         return set_error(NDL_ERR_INVALID_ARG,
-                         "%d rows x %d heads x %d pages need %zu bytes of scratch; the built-in buffer holds %zu",
-                         rows, heads, max_pages, need, kNoAllocScratchBytes);
+                         "%d rows x %d pages need %zu bytes of scratch; the built-in buffer holds %zu", rows,
+                         max_pages, need, kNoAllocScratchBytes);
     void *scratch = nullptr;
-    int st = noalloc_scratch(&scratch);
-    if (st != NDL_OK) return st;
+    rc = noalloc_scratch(&scratch);
+    if (rc != NDL_OK) return rc;
     AttnArgs a{q, qs, row_slot, row_pos, nullptr, page_table, max_pages, pool, (long long)page_bytes, num_pages,
-               layer, heads, rows, kAbiChunkPages, (max_pages + kAbiChunkPages - 1) / kAbiChunkPages,
-               0.125f, out, nullptr, nullptr, status, slots};
-    abi_carve(a, scratch, rows, heads, max_pages);
+               layer, heads, rows, 0.125f, out, status, slots, nullptr, nullptr, nullptr, nullptr};
+    abi_carve(a, scratch, rows, max_pages);
     return launch_attn_decode(a, (cudaStream_t)stream);
 }

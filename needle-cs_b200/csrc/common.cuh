@@ -120,6 +120,19 @@ __device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
     asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
     return r;
 }
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+
+// The single-precision exponential rounded to nearest: the double-precision
+// exp of the (exactly widened) argument, rounded once to float.  The
+// reference's MathF.Exp calls the C runtime's expf, which returns this value
+// except in rare cases within a hair of a rounding midpoint; the CPU oracle
+// uses the same definition, so softmax weights and SiLU gates match bit for
+// bit across the two.
+__device__ __forceinline__ float exp_rn(float x) { return __double2float_rn(exp((double)x)); }
 #endif
 
 // IEEE round-to-nearest-even float -> binary16 (integer-only).

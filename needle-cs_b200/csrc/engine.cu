@@ -52,7 +52,6 @@ enum : uint64_t {
 enum : int { kFCqW, kFCqS, kFCkvW, kFCkvS, kFCoW, kFCoS, kFCrossNorm };
 // fp16 N(0,1) encoder memory of an utterance: stream kStreamMemory + utterance
 constexpr uint64_t kStreamMemory = 1ull << 40;
-constexpr int kAttnChunkPages = 8;  // pages per attention work item (512 positions)
 enum : int { kFQkvW, kFQkvS, kFOW, kFOS, kFGuW, kFGuS, kFDW, kFDS, kFAttnNorm, kFFfnNorm };
 
 struct DeviceLayer {
@@ -97,10 +96,8 @@ struct ndl_engine {
     int32_t *d_meta = nullptr;
     int32_t *h_meta = nullptr;  // pinned staging
     size_t meta_ints = 0;
-    float *partials = nullptr;
-    int *arrivals = nullptr;
-    ndl::AttnWork *attn_work = nullptr, *cross_work = nullptr;  // per-step attention work lists
-    int *n_work = nullptr;                                 // their lengths and counters, int[4] each (self, cross)
+    int32_t *attn_work = nullptr, *cross_work = nullptr;  // per-step attention work lists
+    int *n_work = nullptr;                                // their counters, int[4] each (self, cross)
     int *d_status = nullptr;
     int32_t *d_ids = nullptr;
     float *d_probs = nullptr, *d_logp = nullptr;
@@ -119,7 +116,6 @@ struct ndl_engine {
     uint8_t *d_prefix = nullptr;
     size_t prefix_bytes = 0;
     int last_rows = 0, last_heads = 0;
-    int max_chunks_cap = 0;
     // captured step graphs, keyed by (rows, heads)
     struct StepGraph {
         int rows, heads;
@@ -307,16 +303,12 @@ int build_buffers(ndl_engine *e) {
     TRY(dalloc(e, &e->sa, (size_t)R));
     TRY(dalloc(e, &e->qs, (size_t)R * c.heads));
     TRY(dalloc(e, &e->logits, (size_t)Hd * c.vocab));
-    e->max_chunks_cap = e->max_pages;  // chunk_pages >= 1
-    TRY(dalloc(e, &e->partials, (size_t)R * c.heads * e->max_chunks_cap * kPartialFloats));
-    TRY(dalloc(e, &e->arrivals, (size_t)R * c.heads));
     {
-        const size_t items = (size_t)R * c.heads * ((e->max_pages + kAttnChunkPages - 1) / kAttnChunkPages);
-        TRY(dalloc(e, &e->attn_work, items));
-        if (c.cross) TRY(dalloc(e, &e->cross_work, items));
+        const size_t records = (size_t)R * attn_record_ints(e->max_pages);
+        TRY(dalloc(e, &e->attn_work, records));
+        if (c.cross) TRY(dalloc(e, &e->cross_work, records));
         TRY(dalloc(e, &e->n_work, 8));  // int[4] per list (self, cross)
     }
-    NDL_CUDA(cudaMemsetAsync(e->arrivals, 0, (size_t)R * c.heads * sizeof(int), e->stream));
     TRY(dalloc(e, &e->d_status, 1));
     NDL_CUDA(cudaMemsetAsync(e->d_status, 0, sizeof(int), e->stream));
     // metadata: tokens, slots, positions, order, memory slot, memory position
@@ -484,18 +476,14 @@ int step_kernels(ndl_engine *e, int rows, int heads) {
                                 e->embedding, c.vocab, c.dim, e->x, e->d_status, s));
     }
 
-    // attention split: a fixed number of pages per work item, so that a row's
-    // result depends only on its own length (batch-invariant logits); the
-    // chunk bound comes from the capacity so one captured graph fits any step
-    const int chunk_pages = kAttnChunkPages;
-    const int max_chunks = (e->max_pages + chunk_pages - 1) / chunk_pages;
-    // the work lists (items, page ids) are the same for every layer: built once
+    // the work lists (row records with their page ids) are the same for
+    // every layer: built once per step.  A (row, head) is never split, so a
+    // row's result depends only on its own positions (batch-invariant logits)
     {
         ProfScope p(e, NDL_PROF_PREPARE);
         AttnArgs w{e->q8, e->qs, d_slot, d_pos, d_order, e->d_page_table, e->max_pages, e->pool,
-                   (long long)e->page_bytes, e->ec.kv_pages, 0, c.heads, rows, chunk_pages, max_chunks,
-                   0.0f, e->attn, e->partials, e->arrivals, e->d_status, e->ec.slots, e->qa, e->sa, e->attn_work,
-                   e->n_work};
+                   (long long)e->page_bytes, e->ec.kv_pages, 0, c.heads, rows, 0.0f, e->attn, e->d_status,
+                   e->ec.slots, e->qa, e->sa, e->attn_work, e->n_work};
         TRY(launch_attn_work(w, s));
         if (c.cross) {
             w.row_slot = e->d_meta + e->off_cslot;
@@ -525,16 +513,16 @@ int step_kernels(ndl_engine *e, int rows, int heads) {
             TRY(launch_kv_write(kw, s));
         }
         const AttnArgs aa{e->q8, e->qs, d_slot, d_pos, d_order, e->d_page_table, e->max_pages, e->pool,
-                          (long long)e->page_bytes, e->ec.kv_pages, l, c.heads, rows, chunk_pages, max_chunks,
-                          1.0f / sqrtf((float)c.head_dim), e->attn, e->partials, e->arrivals, e->d_status,
-                          e->ec.slots, e->qa, e->sa, e->attn_work, e->n_work};
+                          (long long)e->page_bytes, e->ec.kv_pages, l, c.heads, rows,
+                          1.0f / sqrtf((float)c.head_dim), e->attn, e->d_status, e->ec.slots, e->qa, e->sa,
+                          e->attn_work, e->n_work};
         {
             ProfScope p(e, NDL_PROF_ATTENTION);
             TRY(launch_attn_decode(aa, s, false, false));
         }
         {
             ProfScope p(e, NDL_PROF_NORM_QUANT);
-            TRY(launch_attn_merge(aa, s));  // merge + quantize of the output into qa, sa
+            TRY(launch_attn_quantize(aa, s));  // the output quantized per row into qa, sa
         }
         {
             ProfScope p(e, NDL_PROF_GEMM_O);
@@ -548,9 +536,9 @@ int step_kernels(ndl_engine *e, int rows, int heads) {
             TRY(ndl_matmul_i8g32(e->qa, e->sa, rows, L.w_cq, L.s_cq, d, d, e->qkv, d, nullptr, nullptr, s));
             TRY(launch_cross_query(e->qkv, d, c.heads, rows, e->q8, e->qs, s));
             AttnArgs ca{e->q8, e->qs, d_cslot, d_cpos, d_order, e->d_page_table, e->max_pages, e->pool,
-                        (long long)e->page_bytes, e->ec.kv_pages, l, c.heads, rows, chunk_pages, max_chunks,
-                        1.0f / sqrtf((float)c.head_dim), e->attn, e->partials, e->arrivals, e->d_status,
-                        e->ec.slots, e->qa, e->sa, e->cross_work, e->n_work + 4};
+                        (long long)e->page_bytes, e->ec.kv_pages, l, c.heads, rows,
+                        1.0f / sqrtf((float)c.head_dim), e->attn, e->d_status, e->ec.slots, e->qa, e->sa,
+                        e->cross_work, e->n_work + 4};
             TRY(launch_attn_decode(ca, s, false));
             TRY(ndl_matmul_i8g32(e->qa, e->sa, rows, L.w_co, L.s_co, d, d, e->x, d, e->x, nullptr, s));
         }
@@ -629,6 +617,9 @@ NDL_API int ndl_engine_create(const ndl_engine_config *ec, const ndl_decoder_con
     NDL_REQUIRE(dc->vocab >= 1, "vocab must be positive");
     NDL_REQUIRE(ec->slots >= 1 && ec->capacity >= kPagePositions && ec->capacity % kPagePositions == 0,
                 "capacity must be a positive multiple of %d", kPagePositions);
+    if (ec->capacity > kAttnMaxPositions)
+        return set_error(NDL_ERR_UNSUPPORTED, "capacity %d: attention holds at most %d positions per row",
+                         ec->capacity, kAttnMaxPositions);
     NDL_REQUIRE(ec->max_rows >= 1 && ec->max_heads >= 1 && ec->max_heads <= ec->max_rows, "bad row limits");
     int count = 0;
     if (cudaGetDeviceCount(&count) != cudaSuccess || ec->device < 0 || ec->device >= count) {
@@ -1111,11 +1102,10 @@ NDL_API int ndl_engine_time_attention(ndl_engine *e, int layer, int reps, float 
     const int rows = e->last_rows;
     const int32_t *d_slot = e->d_meta + e->off_slot, *d_pos = e->d_meta + e->off_pos;
     const int32_t *d_order = e->d_meta + e->off_order;
-    const int max_chunks = (e->max_pages + kAttnChunkPages - 1) / kAttnChunkPages;
     const AttnArgs aa{e->q8, e->qs, d_slot, d_pos, d_order, e->d_page_table, e->max_pages, e->pool,
-                      (long long)e->page_bytes, e->ec.kv_pages, layer, e->dc.heads, rows, kAttnChunkPages,
-                      max_chunks, 1.0f / sqrtf((float)e->dc.head_dim), e->attn, e->partials, e->arrivals,
-                      e->d_status, e->ec.slots, e->qa, e->sa, e->attn_work, e->n_work};
+                      (long long)e->page_bytes, e->ec.kv_pages, layer, e->dc.heads, rows,
+                      1.0f / sqrtf((float)e->dc.head_dim), e->attn, e->d_status, e->ec.slots, e->qa, e->sa,
+                      e->attn_work, e->n_work};
     cudaEvent_t t0 = nullptr, t1 = nullptr;
     NDL_CUDA(cudaEventCreate(&t0));
     NDL_CUDA(cudaEventCreate(&t1));

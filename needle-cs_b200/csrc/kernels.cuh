@@ -51,23 +51,16 @@ int launch_cross_query(const float *q, int ldq, int heads, int rows, int8_t *q8,
 int launch_cross_kv_write(const float *y, int frames, int heads, const int32_t *page_row, int num_pages, uint8_t *pool,
                           long long page_bytes, int layer, int *status, cudaStream_t stream);
 
-constexpr int kPartialFloats = 68;  // 64 outputs + peak + sum, padded to 16 bytes
-
-// One attention work item (row, head, chunk of at most 8 pages) with its
-// page ids resolved: the compacted list of a step's items, in the order the
-// attention kernel deals them, built once per step by launch_attn_work.
-struct AttnWork {
-    int row;
-    int head_chunk;    // head | chunk << 16
-    int len;           // attended positions of the row
-    int pages_chunks;  // pages of this chunk | chunks of the row << 16
-    int page[8];
-};
-static_assert(sizeof(AttnWork) == 48, "three 16-byte loads per item");
-constexpr int kAttnMaxChunkPages = 8;
+// The attention work list: one record per row position of the launch's row
+// order, {row, attended positions, slot, pages (0: an out-of-range row)}
+// followed by the row's page ids, padded to 16 bytes.  Built once per step
+// by launch_attn_work; the kernel deals its (row, head) items dynamically.
+__host__ __device__ __forceinline__ int attn_record_ints(int max_pages) { return 4 + ((max_pages + 3) & ~3); }
+// Positions one (row, head) may attend to: its scores stay in shared memory.
+constexpr int kAttnMaxPositions = 8192;
 
 struct AttnArgs {
-    const int8_t *q;  // [rows][heads][64]
+    const int8_t *q;  // [rows][heads][64], dims in k_slot order
     const float *qs;  // [rows][heads]
     const int32_t *row_slot, *row_pos, *row_order;
     const int32_t *page_table;
@@ -76,19 +69,16 @@ struct AttnArgs {
     long long page_bytes;
     int num_pages;
     int layer, heads, rows;
-    int chunk_pages, max_chunks;
     float inv_sqrt_d;
     float *out;       // [rows][heads][64]
-    float *partials;  // [rows][heads][max_chunks][kPartialFloats]
-    int *arrivals;    // unused (kept for layout stability)
     int *status;
     int slots;        // rows of page_table (bounds check)
     // nullable: the row's heads x 64 outputs quantized per row
-    // (Scalar.QuantizeInt8), the o-projection's input, in the merge launch
+    // (Scalar.QuantizeInt8), the o-projection's input
     int8_t *q_out;    // [rows][heads * 64]
     float *s_out;     // [rows]
-    AttnWork *work;   // [rows * heads * max_chunks] items, compacted
-    int *n_work;      // int[4]: the list's length, the next dynamically dealt item, finished CTAs, unused
+    int32_t *work;    // [rows][attn_record_ints(max_pages)]
+    int *n_work;      // int[4]: the item count, the next dynamically dealt item, finished CTAs, unused
 };
 // Primed-prefix blobs (prefix.cu): bytes of a blob of `len` positions, and
 // the move of a slot's first `len` positions between its pages and a blob
@@ -97,14 +87,14 @@ size_t prefix_blob_bytes(int layers, int heads, int len);
 int launch_prefix_move(bool to_blob, int layers, int heads, int len, const int32_t *pages, uint8_t *pool,
                        long long page_bytes, int num_pages, uint8_t *blob, int *status, cudaStream_t stream);
 
-// Builds the compacted work list of a launch shape (one small launch; the
-// engine builds it once per step and reuses it for every layer).
+// Builds the work list of a launch shape (one small launch; the engine
+// builds it once per step and reuses it for every layer).
 int launch_attn_work(const AttnArgs &a, cudaStream_t stream);
 // build_work: launch_attn_work first (callers without a prebuilt list);
-// merge: also launch the merge (and quantize, when q_out is set) after it.
-int launch_attn_decode(const AttnArgs &a, cudaStream_t stream, bool build_work = true, bool merge = true);
-// The merge of long rows' chunk partials (+ the per-row quantize into q_out).
-int launch_attn_merge(const AttnArgs &a, cudaStream_t stream);
+// quantize: also quantize the outputs per row into q_out, s_out after it.
+int launch_attn_decode(const AttnArgs &a, cudaStream_t stream, bool build_work = true, bool quantize = true);
+// The per-row quantize of the attention outputs into q_out, s_out.
+int launch_attn_quantize(const AttnArgs &a, cudaStream_t stream);
 
 // Streaming int8 GEMV (mma.sync m16n8k32 per 32-column group), any m.
 int launch_gemv_i8g32(const MatmulArgs &a, cudaStream_t stream);

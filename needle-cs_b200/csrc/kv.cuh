@@ -1,19 +1,23 @@
 // Paged int8 KV cache layout and the PTX helpers the attention kernels use.
 //
 // A page holds 64 consecutive positions of one slot for every layer.  Inside
-// a page, the block of (layer, head) is one contiguous 8704-byte record
-//     [K int8 64x64][K scale f32 x64][V^T int8 64x64][V scale f32 x64]
-// so a single 16-byte-aligned bulk copy brings everything attention needs
-// for 64 positions of one head into shared memory.  This replaces the
-// reference's flat per-slot arrays [layer][capacity][kvWidth] + scales
-// (src/Needle/Engine.cs:184-187,220-223) with the same per-(position, head)
-// int8 + fp32-scale contents, rearranged for the tensor-core fragments:
-//  * K (row = position, col = dim) and V^T (row = dim, col = pv_col of the
-//    position) are int8 64x64 matrices stored in m16n8k32 A-fragment order
-//    (frag_byte): a lane's four A registers of one (16-row tile, 32-col
-//    k-step) are one 16-byte chunk and a warp reads 512 contiguous bytes;
-//  * the scales of position p sit at scale_slot(p), so the lane that owns
-//    p's score reads its two scales as one float2.
+// a page, the block of (layer, head) is one contiguous 8704-byte record of
+// two 4352-byte halves:
+//     K half: [K int8 64x64][K scale f32 x64]
+//     V half: [V scale f32 x64][V int8 64x64]
+// so one 16-byte-aligned bulk copy brings either half of 64 positions of one
+// head into shared memory.  This replaces the reference's flat per-slot
+// arrays [layer][capacity][kvWidth] + scales (src/Needle/Engine.cs:184-187,
+// 220-223) with the same per-(position, head) int8 + fp32-scale contents:
+//  * K (row = position, col = dim) is an int8 64x64 matrix in m16n8k32
+//    A-fragment order (frag_byte): a lane's four A registers of one (16-row
+//    tile, 32-col k-step) are one 16-byte chunk and a warp reads 512
+//    contiguous bytes; the K scale of position p sits at scale_slot(p), so
+//    the lane that owns p's score reads its scale pair as one float2;
+//  * V is stored dim-major, 64 positions of one dim in 64 bytes, its four
+//    16-byte chunks rotated by (dim >> 1) & 3 so that eight lanes reading
+//    chunk c of eight consecutive dims hit eight distinct bank groups; the V
+//    scales are in position order.
 // The query vector is stored with its dims in k_slot order: a lane's
 // m16n8k32 B registers for both k-steps are one 16-byte chunk.
 #pragma once
@@ -25,9 +29,10 @@ namespace ndl {
 constexpr int kPagePositions = 64;
 constexpr int kHeadDim = 64;
 constexpr int kKvBlockBytes = 2 * (kPagePositions * kHeadDim + kPagePositions * 4);  // 8704
+constexpr int kKvHalfBytes = kKvBlockBytes / 2;                                       // 4352
 constexpr int kKScaleOffset = kPagePositions * kHeadDim;                              // 4096
-constexpr int kVOffset = kKScaleOffset + kPagePositions * 4;                          // 4352
-constexpr int kVScaleOffset = kVOffset + kPagePositions * kHeadDim;                   // 8448
+constexpr int kVScaleOffset = kKvHalfBytes;                                           // 4352
+constexpr int kVOffset = kVScaleOffset + kPagePositions * 4;                          // 4608
 
 __host__ __device__ __forceinline__ int k_slot(int d) { return ((d & 15) >> 2) * 16 + (d >> 4) * 4 + (d & 3); }
 
@@ -39,16 +44,14 @@ __host__ __device__ __forceinline__ int frag_byte(int row, int col) {
            (((row >> 3) & 1) + 2 * ((col >> 4) & 1)) * 4 + (col & 3);
 }
 // The QK step leaves position p's score with lane 4*(p&7) + (p>>4&3) (half
-// p>>3&1).  pv_col(p) is p's column in the PV product, chosen so that the
-// eight lanes sharing p>>4&3 hold exactly the sixteen positions of the
-// B fragment that lanes with that thread-in-group index read.
-__host__ __device__ __forceinline__ int pv_col(int p) {
-    const int g = p & 7;
-    return 32 * (g >> 2) + 16 * ((g >> 1) & 1) + 4 * ((p >> 4) & 3) + 2 * (g & 1) + ((p >> 3) & 1);
-}
+// p>>3&1); its K scale sits at that lane's float2.
 __host__ __device__ __forceinline__ int scale_slot(int p) { return 2 * ((p & 7) * 4 + ((p >> 4) & 3)) + ((p >> 3) & 1); }
 __host__ __device__ __forceinline__ int k_byte(int p, int d) { return frag_byte(p, d); }
-__host__ __device__ __forceinline__ int v_byte(int p, int d) { return kVOffset + frag_byte(d, pv_col(p)); }
+__host__ __device__ __forceinline__ int k_scale_index(int p) { return scale_slot(p); }
+__host__ __device__ __forceinline__ int v_scale_index(int p) { return p; }
+__host__ __device__ __forceinline__ int v_byte(int p, int d) {
+    return kVOffset + d * 64 + ((((p >> 4) ^ ((d >> 1) & 3)) << 4) | (p & 15));
+}
 
 __host__ __device__ __forceinline__ size_t kv_page_bytes(int layers, int heads) {
     return (size_t)layers * heads * kKvBlockBytes;

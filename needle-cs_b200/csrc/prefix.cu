@@ -35,8 +35,8 @@ __global__ void __launch_bounds__(1024) prefix_move_kernel(bool to_blob, int lay
     uint8_t *vq = kq + (size_t)len * row;
     float *ks = reinterpret_cast<float *>(base + 2 * (size_t)len * row) + (size_t)pos * heads + h;
     float *vs = ks + (size_t)len * heads;
-    float *kso = reinterpret_cast<float *>(blk + kKScaleOffset) + scale_slot(j);
-    float *vso = reinterpret_cast<float *>(blk + kVScaleOffset) + scale_slot(j);
+    float *kso = reinterpret_cast<float *>(blk + kKScaleOffset) + k_scale_index(j);
+    float *vso = reinterpret_cast<float *>(blk + kVScaleOffset) + v_scale_index(j);
     if (to_blob) {
         *kq = blk[k_byte(j, d)];
         *vq = blk[v_byte(j, d)];

@@ -1,12 +1,13 @@
 // Row quantizers: the reference's per-row int8 activation quantizer and the
 // fused RMSNorm -> quantize prologue of every synthetic-decoder linear.
 //
-// One warp per row.  The peak is an exact max (order-free); scale, inverse
-// and every product use round-to-nearest intrinsics, so the int8 values and
-// the fp32 scale are bit-identical to Scalar.QuantizeInt8
-// (src/Needle/Scalar.cs:67-74).  The RMSNorm sum of squares is a warp tree
-// (the reference sums left to right), so the normalised row can differ from
-// the scalar one in the last ulp.
+// The peak is an exact max (order-free); scale, inverse and every product
+// use round-to-nearest intrinsics, so the int8 values and the fp32 scale are
+// bit-identical to Scalar.QuantizeInt8 (src/Needle/Scalar.cs:67-74).  The
+// RMSNorm sum of squares runs left to right on one lane, as
+// Scalar.SumOfSquares does (src/Needle/Scalar.cs:206-211), from squares the
+// other lanes compute, so the normalised row is the scalar one bit for bit.
+// SiLU's exponential is exp_rn, the correctly rounded one.
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -17,10 +18,17 @@ __device__ __forceinline__ float warp_max(float v) {
     for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
     return v;
 }
-__device__ __forceinline__ float warp_sum(float v) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
-    return v;
+
+// Ops.InverseRms (src/Needle/Ops.cs:209, epsilon 1e-6): 1/sqrt(sum/n + eps)
+// with the sum of squares taken left to right by lane 0 of the warp (the
+// row is read from global memory; a fallback path for shapes the CTA
+// kernel cannot hold).
+__device__ __forceinline__ float inverse_rms_in_order(const float *row, int cols, int lane) {
+    float ss = 0.0f;
+    if (lane == 0)
+        for (int c = 0; c < cols; c++) ss = __fadd_rn(ss, __fmul_rn(row[c], row[c]));
+    ss = __shfl_sync(0xffffffffu, ss, 0);
+    return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)cols), 1e-6f)));
 }
 
 __device__ __forceinline__ int8_t quantize_one(float x, float inverse) {
@@ -48,18 +56,7 @@ __global__ void __launch_bounds__(256) quantize_rows_vec_kernel(const float *__r
     const float *row = x + (size_t)warp * cols;
     int8_t *out = q + (size_t)warp * cols;
     float inv_rms = 1.0f;
-    if (MODE == 1) {
-        float ss = 0.0f;
-        for (int c = lane * 4; c < cols; c += 128) {
-            float4 v = *reinterpret_cast<const float4 *>(row + c);
-            ss = __fadd_rn(ss, __fmul_rn(v.x, v.x));
-            ss = __fadd_rn(ss, __fmul_rn(v.y, v.y));
-            ss = __fadd_rn(ss, __fmul_rn(v.z, v.z));
-            ss = __fadd_rn(ss, __fmul_rn(v.w, v.w));
-        }
-        ss = warp_sum(ss);
-        inv_rms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)cols), 1e-6f)));
-    }
+    if (MODE == 1) inv_rms = inverse_rms_in_order(row, cols, lane);
     float peak = 0.0f;
     for (int c = lane * 16; c < cols; c += 512) {
 #pragma unroll
@@ -112,12 +109,7 @@ __global__ void __launch_bounds__(256) quantize_rows_scalar_kernel(const float *
     const float *row = x + (size_t)warp * cols;
     int8_t *out = q + (size_t)warp * cols;
     float inv_rms = 1.0f;
-    if (MODE == 1) {
-        float ss = 0.0f;
-        for (int c = lane; c < cols; c += 32) ss = __fadd_rn(ss, __fmul_rn(row[c], row[c]));
-        ss = warp_sum(ss);
-        inv_rms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)cols), 1e-6f)));
-    }
+    if (MODE == 1) inv_rms = inverse_rms_in_order(row, cols, lane);
     float peak = 0.0f;
     for (int c = lane; c < cols; c += 32) {
         float v = row[c];
@@ -148,6 +140,7 @@ __global__ void __launch_bounds__(kRowThreads) row_quantize_kernel(const float *
                                                                    float *__restrict__ scales) {
     pdl_enter();
     __shared__ float red[kRowThreads / 32];
+    __shared__ float4 squares[MODE == 1 ? kRowThreads * kRowMaxVec : 1];
     const int row = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const float4 *in = reinterpret_cast<const float4 *>(x + (size_t)row * ld_in);
     const int nv = cols >> 2;
@@ -168,25 +161,36 @@ __global__ void __launch_bounds__(kRowThreads) row_quantize_kernel(const float *
                 const float *uu = reinterpret_cast<const float *>(&u);
 #pragma unroll
                 for (int e = 0; e < 4; e++) {
-                    const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g[e])));
+                    const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, exp_rn(-g[e])));
                     g[e] = __fmul_rn(__fmul_rn(g[e], sig), uu[e]);
                 }
             }
         }
     }
     if (MODE == 1) {
-        float ss = 0.0f;
+        // squares in element order through shared memory, summed left to
+        // right by one thread (Scalar.SumOfSquares)
 #pragma unroll
         for (int i = 0; i < kRowMaxVec; i++) {
-            ss = __fadd_rn(ss, __fmul_rn(v[i].x, v[i].x));
-            ss = __fadd_rn(ss, __fmul_rn(v[i].y, v[i].y));
-            ss = __fadd_rn(ss, __fmul_rn(v[i].z, v[i].z));
-            ss = __fadd_rn(ss, __fmul_rn(v[i].w, v[i].w));
+            const int idx = tid + i * kRowThreads;
+            if (idx < nv)
+                squares[idx] = make_float4(__fmul_rn(v[i].x, v[i].x), __fmul_rn(v[i].y, v[i].y),
+                                           __fmul_rn(v[i].z, v[i].z), __fmul_rn(v[i].w, v[i].w));
         }
-        ss = warp_sum(ss);
-        if (lane == 0) red[warp] = ss;
         __syncthreads();
-        ss = __fadd_rn(__fadd_rn(red[0], red[1]), __fadd_rn(red[2], red[3]));
+        if (tid == 0) {
+            float ss = 0.0f;
+            for (int i = 0; i < nv; i++) {
+                const float4 q4 = squares[i];
+                ss = __fadd_rn(ss, q4.x);
+                ss = __fadd_rn(ss, q4.y);
+                ss = __fadd_rn(ss, q4.z);
+                ss = __fadd_rn(ss, q4.w);
+            }
+            red[0] = ss;
+        }
+        __syncthreads();
+        const float ss = red[0];
         __syncthreads();
         const float inv_rms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)cols), 1e-6f)));
         const float4 *wv = reinterpret_cast<const float4 *>(weight);

@@ -65,7 +65,7 @@ __global__ void __launch_bounds__(256) swiglu_quantize_kernel(const float *__res
     float peak = 0.0f;
     for (int i = lane; i < ffn; i += 32) {
         const float gv = g[i];
-        const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-gv)));
+        const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, exp_rn(-gv)));
         const float v = __fmul_rn(__fmul_rn(gv, sig), u[i]);
         a[i] = v;
         peak = fmaxf(peak, fabsf(v));
@@ -302,11 +302,11 @@ __global__ void __launch_bounds__(256) kv_fill_kernel(uint64_t key, int layers, 
     if (kind == 0) {
         blk[k_byte(j, lane)] = (uint8_t)q0;
         blk[k_byte(j, lane + 32)] = (uint8_t)q1;
-        if (lane == 0) reinterpret_cast<float *>(blk + kKScaleOffset)[scale_slot(j)] = scale;
+        if (lane == 0) reinterpret_cast<float *>(blk + kKScaleOffset)[k_scale_index(j)] = scale;
     } else {
         blk[v_byte(j, lane)] = (uint8_t)q0;
         blk[v_byte(j, lane + 32)] = (uint8_t)q1;
-        if (lane == 0) reinterpret_cast<float *>(blk + kVScaleOffset)[scale_slot(j)] = scale;
+        if (lane == 0) reinterpret_cast<float *>(blk + kVScaleOffset)[v_scale_index(j)] = scale;
     }
 }
 

@@ -98,6 +98,15 @@ static float round_even(float x) {
     return t - kRoundBias;
 }
 
+/* MathF.Exp: the single-precision exponential rounded to nearest, computed
+ * as the double-precision exp of the exactly widened argument, rounded once
+ * to float.  .NET's MathF.Exp calls the C runtime's expf, which returns this
+ * value except in rare cases within a hair of a rounding midpoint (the
+ * reference pins its own exp only to a tolerance,
+ * tests/Needle.Tests/KernelTests.cs:35-46).  The device kernels use the same
+ * definition, so softmax weights and SiLU gates compare bit for bit. */
+static float exp_rn(float x) { return (float)exp((double)x); }
+
 static float maxf_cs(float a, float b) { return a > b ? a : (b > a ? b : (a == a ? a : b)); }
 
 /* Scalar.AbsMax (Scalar.cs:55-60). */
@@ -184,7 +193,7 @@ void ndo_planes(const int8_t *quantized, int bits, int8_t *dst, int *sum) {
 }
 
 /* Scalar.Sigmoid (Scalar.cs:194). */
-float ndo_sigmoid(float x) { return 1.0f / (1.0f + expf(-x)); }
+float ndo_sigmoid(float x) { return 1.0f / (1.0f + exp_rn(-x)); }
 
 /* Scalar.Softmax (Scalar.cs:220-231). */
 void ndo_softmax(float *s, int n) {
@@ -192,7 +201,7 @@ void ndo_softmax(float *s, int n) {
     for (int i = 0; i < n; i++) peak = maxf_cs(peak, s[i]);
     float total = 0.0f;
     for (int i = 0; i < n; i++) {
-        s[i] = expf(s[i] - peak);
+        s[i] = exp_rn(s[i] - peak);
         total += s[i];
     }
     for (int i = 0; i < n; i++) s[i] /= total;
@@ -295,7 +304,7 @@ void ndo_taps3(const float *taps, int width, const float *current, float *dst) {
 void ndo_sinkhorn4x4(const float *logits, float *result) {
     for (int r = 0; r < 4; r++) {
         float peak = maxf_cs(maxf_cs(logits[r * 4], logits[r * 4 + 1]), maxf_cs(logits[r * 4 + 2], logits[r * 4 + 3]));
-        for (int c = 0; c < 4; c++) result[r * 4 + c] = expf(logits[r * 4 + c] - peak);
+        for (int c = 0; c < 4; c++) result[r * 4 + c] = exp_rn(logits[r * 4 + c] - peak);
     }
     for (int it = 0; it < 20; it++) {
         for (int r = 0; r < 4; r++) {
@@ -522,12 +531,12 @@ void ndo_conf_pool_update(int row, const float *streams, const int32_t *row_slot
                 }
                 float score = dot_seq(c, probe_vectors + (size_t)index * dim, dim) * inverse_root;
                 if (score > mx[index]) {
-                    float rescale = expf(mx[index] - score);
+                    float rescale = exp_rn(mx[index] - score);
                     sm[index] = sm[index] * rescale + 1.0f;
                     for (int i = 0; i < dim; i++) acc[i] = rescale * acc[i] + 1.0f * c[i];
                     mx[index] = score;
                 } else {
-                    float weight = expf(score - mx[index]);
+                    float weight = exp_rn(score - mx[index]);
                     sm[index] += weight;
                     for (int i = 0; i < dim; i++) acc[i] += weight * c[i];
                 }
@@ -737,7 +746,7 @@ void ndo_merge_partials(const float *partials, int count, int heads, int stride,
             float peak0 = partials[peak_off + h];
             float peak1 = partials[stride + peak_off + h];
             float pk = maxf_cs(peak0, peak1);
-            float w0 = expf(peak0 - pk), w1 = expf(peak1 - pk);
+            float w0 = exp_rn(peak0 - pk), w1 = exp_rn(peak1 - pk);
             float tot = 0.0f;
             tot += w0 * partials[peak_off + 8 + h];
             tot += w1 * partials[stride + peak_off + 8 + h];
@@ -750,7 +759,7 @@ void ndo_merge_partials(const float *partials, int count, int heads, int stride,
         for (int c = 0; c < count; c++) peak = maxf_cs(peak, partials[c * stride + peak_off + h]);
         float total = 0.0f;
         for (int c = 0; c < count; c++) {
-            weights[c] = expf(partials[c * stride + peak_off + h] - peak);
+            weights[c] = exp_rn(partials[c * stride + peak_off + h] - peak);
             total += weights[c] * partials[c * stride + peak_off + 8 + h];
         }
         float inverse = 1.0f / total;
@@ -806,7 +815,7 @@ int ndo_argmax_masked(const float *x, const uint32_t *mask, int words, int lengt
 /* Ops.ScalarBestProbability (Ops.cs:1530-1535). */
 float ndo_best_probability(const float *values, int count, float best) {
     float total = 0.0f;
-    for (int i = 0; i < count; i++) total += expf(values[i] - best);
+    for (int i = 0; i < count; i++) total += exp_rn(values[i] - best);
     return 1.0f / total;
 }
 
@@ -892,7 +901,7 @@ void ndo_topk_logsoftmax(const float *x, int n, int k, int *indices, float *log_
         indices[m] = top_idx[m];
         float lp = top_val[m] - log_shift;
         log_probs[m] = lp;
-        if (probs) probs[m] = expf(lp);
+        if (probs) probs[m] = exp_rn(lp);
     }
 }
 

@@ -17,19 +17,23 @@ def frag_byte(row, col):
             + (((row >> 3) & 1) + 2 * ((col >> 4) & 1)) * 4 + (col & 3))
 
 
-def pv_col(p):
-    g = p & 7
-    return 32 * (g >> 2) + 16 * ((g >> 1) & 1) + 4 * ((p >> 4) & 3) + 2 * (g & 1) + ((p >> 3) & 1)
-
-
 def scale_slot(p):
+    """Index of position p's K scale (the lane order of the QK results)."""
     return 2 * ((p & 7) * 4 + ((p >> 4) & 3)) + ((p >> 3) & 1)
 
 
+def v_byte(p, d):
+    """Byte of (position p, dim d) within a page's V matrix: dim-major, the
+    four 16-byte position chunks of dim d rotated by (d >> 1) & 3."""
+    return d * 64 + ((((p >> 4) ^ ((d >> 1) & 3)) << 4) | (p & 15))
+
+
+# a (layer, head) record: K half [K 0:4096][K scales 4096:4352], V half [V scales 4352:4608][V 4608:8704]
+K_OFF, KS_OFF, VS_OFF, V_OFF = 0, 4096, 4352, 4608
 K_ORDER = np.array([k_slot(d) for d in range(64)])
 K_BYTE = np.array([[frag_byte(p, d) for d in range(64)] for p in range(64)])  # [position][dim] -> byte
-V_BYTE = np.array([[frag_byte(d, pv_col(p)) for d in range(64)] for p in range(64)])  # within the V block
-S_SLOT = np.array([scale_slot(p) for p in range(64)])
+V_BYTE = np.array([[v_byte(p, d) for d in range(64)] for p in range(64)])  # within the V matrix
+S_SLOT = np.array([scale_slot(p) for p in range(64)])  # K scales
 
 
 def make_case(seed, lengths, heads, layers=2, layer=1, max_pages=17):
@@ -56,16 +60,16 @@ def make_case(seed, lengths, heads, layers=2, layer=1, max_pages=17):
                 blk = pool[base:base + BLOCK]
                 kr = np.zeros(4096, np.uint8)
                 kr[K_BYTE[:cnt]] = K[s, lo:hi, h].view(np.uint8)
-                blk[:4096] = kr
+                blk[K_OFF:K_OFF + 4096] = kr
                 ks = np.zeros(64, np.float32)
                 ks[S_SLOT[:cnt]] = KS[s, lo:hi, h]
-                blk[4096:4352] = ks.view(np.uint8)
-                vt = np.zeros(4096, np.uint8)
-                vt[V_BYTE[:cnt]] = V[s, lo:hi, h].view(np.uint8)
-                blk[4352:8448] = vt
+                blk[KS_OFF:KS_OFF + 256] = ks.view(np.uint8)
                 vs = np.zeros(64, np.float32)
-                vs[S_SLOT[:cnt]] = VS[s, lo:hi, h]
-                blk[8448:8704] = vs.view(np.uint8)
+                vs[:cnt] = VS[s, lo:hi, h]
+                blk[VS_OFF:VS_OFF + 256] = vs.view(np.uint8)
+                vm = np.zeros(4096, np.uint8)
+                vm[V_BYTE[:cnt]] = V[s, lo:hi, h].view(np.uint8)
+                blk[V_OFF:V_OFF + 4096] = vm
     q_perm = np.zeros((rows, heads, 64), np.int8)
     q_perm[:, :, K_ORDER] = Q
     page_table = np.array([[s * max_pages + i for i in range(max_pages)] for s in range(rows)], np.int32)

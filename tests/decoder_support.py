@@ -2,7 +2,7 @@
 the CPU oracle and regenerate the synthetic prefix K/V on the host."""
 import numpy as np
 
-from attention_support import K_BYTE, S_SLOT, V_BYTE
+from attention_support import K_BYTE, K_OFF, KS_OFF, S_SLOT, V_BYTE, V_OFF, VS_OFF
 from conftest import entry
 
 KV_STREAM_SHIFT = 20
@@ -41,8 +41,9 @@ def prefix_kv(ops, oracle, decoder, kv, count, seed, session):
 def read_slot_kv(engine, slot, positions):
     """Reads positions [0, positions) of a slot from the paged pool into the
     flat reference layout (k, v int8 [layers][positions][H*64]; ks, vs).
-    Page record of (layer, head): K and V^T int8 in m16n8k32 A-fragment
-    order (K_BYTE, V_BYTE), scales at S_SLOT."""
+    Page record of (layer, head): K int8 in m16n8k32 A-fragment order
+    (K_BYTE) with its scales at S_SLOT, then the V scales in position order
+    and V dim-major (V_BYTE)."""
     cfg = engine.model
     H, L = cfg.heads, cfg.layers
     page_bytes = engine.page_bytes()
@@ -58,10 +59,10 @@ def read_slot_kv(engine, slot, positions):
         for l in range(L):
             for h in range(H):
                 blk = pool[page * page_bytes + (l * H + h) * 8704:][:8704]
-                out["k"][l, lo:hi, h * 64:(h + 1) * 64] = blk[:4096][K_BYTE[:n]].view(np.int8)
-                out["ks"][l, lo:hi, h] = blk[4096:4352].view(np.float32)[S_SLOT[:n]]
-                out["v"][l, lo:hi, h * 64:(h + 1) * 64] = blk[4352:8448][V_BYTE[:n]].view(np.int8)
-                out["vs"][l, lo:hi, h] = blk[8448:8704].view(np.float32)[S_SLOT[:n]]
+                out["k"][l, lo:hi, h * 64:(h + 1) * 64] = blk[K_OFF:K_OFF + 4096][K_BYTE[:n]].view(np.int8)
+                out["ks"][l, lo:hi, h] = blk[KS_OFF:KS_OFF + 256].view(np.float32)[S_SLOT[:n]]
+                out["vs"][l, lo:hi, h] = blk[VS_OFF:VS_OFF + 256].view(np.float32)[:n]
+                out["v"][l, lo:hi, h * 64:(h + 1) * 64] = blk[V_OFF:V_OFF + 4096][V_BYTE[:n]].view(np.int8)
     return out
 
 

@@ -1,7 +1,10 @@
 """Standalone paged decode attention (ndl_attention_paged) against the
-oracle's Scalar.AttentionHead restatement.  Tolerance: the reference's
-AttentionTile conformance bar, 5e-5 x peak |output|
-(tests/Needle.Tests/Conformance/KernelConformanceTests.cs:440-447)."""
+oracle's Scalar.AttentionHead restatement: bit-identical.  The kernel keeps
+the reference's order of every rounding (scores, max, exponentials, the
+total summed in position order, p = e / total, out += (p * vs) * v in
+position order), so no tolerance is needed; the reference's own
+AttentionTile conformance bar would be 3e-5 x peak |output|
+(tests/Needle.Tests/KernelTests.cs:231-236)."""
 import numpy as np
 import pytest
 import torch
@@ -30,8 +33,7 @@ def test_paged_attention_matches_oracle(ops, oracle, cuda, heads):
     got = _run(ops, cuda, case)
     ref = oracle_out(oracle, case, LENGTHS)
     for r in range(len(LENGTHS)):
-        peak = np.abs(ref[r]).max()
-        assert np.all(np.abs(got[r] - ref[r]) <= 5e-5 * peak), (LENGTHS[r], np.abs(got[r] - ref[r]).max() / peak)
+        assert np.array_equal(got[r], ref[r]), (LENGTHS[r], np.abs(got[r] - ref[r]).max() / np.abs(ref[r]).max())
 
 
 def test_paged_attention_caller_workspace(ops, cuda):
@@ -68,6 +70,4 @@ def test_paged_attention_on_a_second_device(ops, oracle, cuda):
     with torch.cuda.device(second_dev):
         second = _run(ops, second_dev, case)
     assert np.array_equal(first, second)
-    for r in range(len(lengths)):
-        peak = np.abs(ref[r]).max()
-        assert np.all(np.abs(second[r] - ref[r]) <= 5e-5 * peak), lengths[r]
+    assert np.array_equal(second, ref)
