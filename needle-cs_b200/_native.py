@@ -77,6 +77,7 @@ SIGNATURES = {
     "ndl_engine_free_pages": (c_int, [c_void_p, ctypes.POINTER(c_int)]),
     "ndl_engine_time_attention": (c_int, [c_void_p, c_int, c_int, ctypes.POINTER(c_float)]),
     "ndl_selftest_bounded_wait": (c_int, [c_int]),
+    "ndl_selftest_exp": (c_int, [c_void_p, c_int, c_void_p, c_void_p]),
     "ndl_kt_quantize_int8": (c_float, [c_void_p, c_int, c_void_p]),
     "ndl_kt_argmax_masked": (c_int, [c_void_p, c_void_p, c_int, c_int]),
     "ndl_kt_best_probability": (c_float, [c_void_p, c_int, c_float]),

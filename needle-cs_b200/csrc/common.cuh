@@ -126,13 +126,42 @@ __device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
     return r;
 }
 
-// The single-precision exponential rounded to nearest: the double-precision
-// exp of the (exactly widened) argument, rounded once to float.  The
-// reference's MathF.Exp calls the C runtime's expf, which returns this value
-// except in rare cases within a hair of a rounding midpoint; the CPU oracle
-// uses the same definition, so softmax weights and SiLU gates match bit for
-// bit across the two.
-__device__ __forceinline__ float exp_rn(float x) { return __double2float_rn(exp((double)x)); }
+// exp of a float, rounded to nearest float: the reference's MathF.Exp,
+// which calls the C runtime's expf (a nearly correctly rounded function).
+// Computed here in double precision from the mathematics, with IEEE
+// operations only, so that the CPU oracle, which restates the same steps,
+// gets the same bits: Cody and Waite's argument reduction
+// x = k*ln2 + r, k = rint(x/ln2), with ln2 split into a high part whose
+// products with k are exact and a low part (the split published with
+// fdlibm), then exp(r) by its Taylor series to degree 13 in Horner form with
+// fused multiply-adds, scaled by 2^k (exact) and rounded once to float.  The
+// relative error before that rounding is below 1e-15, so the result is the
+// correctly rounded float unless exp(x) lies within about 1e-15 of a
+// rounding midpoint.
+__device__ __forceinline__ float exp_rn(float x) {
+    if (x != x) return x;
+    if (x > 89.0f) return __int_as_float(0x7f800000);  // above the float range
+    if (x < -104.0f) return 0.0f;                        // below half the smallest subnormal
+    const double xd = (double)x;
+    const double k = rint(__dmul_rn(xd, 1.4426950408889634));
+    const double r = __dsub_rn(__dsub_rn(xd, __dmul_rn(k, 6.93147180369123816490e-01)),
+                               __dmul_rn(k, 1.90821492927058770002e-10));
+    double p = 1.6059043836821614599e-10;   // 1/13!
+    p = __fma_rn(p, r, 2.0876756987868098979e-09);   // 1/12!
+    p = __fma_rn(p, r, 2.5052108385441718775e-08);   // 1/11!
+    p = __fma_rn(p, r, 2.7557319223985890653e-07);   // 1/10!
+    p = __fma_rn(p, r, 2.7557319223985890653e-06);   // 1/9!
+    p = __fma_rn(p, r, 2.4801587301587301587e-05);   // 1/8!
+    p = __fma_rn(p, r, 1.9841269841269841270e-04);   // 1/7!
+    p = __fma_rn(p, r, 1.3888888888888888889e-03);   // 1/6!
+    p = __fma_rn(p, r, 8.3333333333333333333e-03);   // 1/5!
+    p = __fma_rn(p, r, 4.1666666666666666667e-02);   // 1/4!
+    p = __fma_rn(p, r, 1.6666666666666666667e-01);   // 1/3!
+    p = __fma_rn(p, r, 0.5);
+    p = __fma_rn(p, r, 1.0);
+    p = __fma_rn(p, r, 1.0);
+    return __double2float_rn(scalbn(p, (int)k));
+}
 #endif
 
 // IEEE round-to-nearest-even float -> binary16 (integer-only).

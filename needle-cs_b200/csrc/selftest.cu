@@ -21,6 +21,11 @@ __global__ void bounded_wait_kernel(uint32_t tests, int *status) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&bar)) : "memory");
 }
 
+__global__ void exp_kernel(const float *x, int n, float *y) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) y[i] = exp_rn(x[i]);
+}
+
 }  // namespace
 
 extern "C" {
@@ -44,6 +49,15 @@ NDL_API int ndl_selftest_bounded_wait(int tests) {
     if (st != NDL_OK) return st;
     if (h & kStatusTimeout) return set_error(NDL_ERR_TIMEOUT, "a kernel wait gave up after %d tests", tests);
     return NDL_OK;
+}
+
+// exp_rn, the library's float exponential (the one its softmax and SiLU
+// use), over n device floats: lets a test pin it to the CPU oracle's.
+NDL_API int ndl_selftest_exp(const float *x, int n, float *y, void *stream) {
+    NDL_REQUIRE(n >= 0 && (n == 0 || (x && y)), "bad arguments");
+    if (n == 0) return NDL_OK;
+    exp_kernel<<<(n + 255) / 256, 256, 0, (cudaStream_t)stream>>>(x, n, y);
+    return check_launch("selftest_exp");
 }
 
 }  // extern "C"

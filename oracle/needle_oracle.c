@@ -98,14 +98,46 @@ static float round_even(float x) {
     return t - kRoundBias;
 }
 
-/* MathF.Exp: the single-precision exponential rounded to nearest, computed
- * as the double-precision exp of the exactly widened argument, rounded once
- * to float.  .NET's MathF.Exp calls the C runtime's expf, which returns this
- * value except in rare cases within a hair of a rounding midpoint (the
- * reference pins its own exp only to a tolerance,
- * tests/Needle.Tests/KernelTests.cs:35-46).  The device kernels use the same
- * definition, so softmax weights and SiLU gates compare bit for bit. */
-static float exp_rn(float x) { return (float)exp((double)x); }
+/* MathF.Exp (.NET calls the C runtime's expf): exp of a float rounded to
+ * nearest float, computed in double precision from the mathematics with
+ * IEEE operations only.  Cody and Waite's argument reduction x = k*ln2 + r,
+ * k = rint(x/ln2), with ln2 split into a high part whose products with k are
+ * exact and a low part (the split published with fdlibm); exp(r) by its
+ * Taylor series to degree 13 in Horner form with fused multiply-adds; scaled
+ * by 2^k (exact) and rounded once to float.  The relative error before that
+ * rounding is below 1e-15: the correctly rounded float unless exp(x) lies
+ * within about 1e-15 of a rounding midpoint, where a C runtime's expf may
+ * differ as well (the reference pins its own exp only to a tolerance,
+ * tests/Needle.Tests/KernelTests.cs:35-46).  The CUDA kernels evaluate the
+ * same steps, so softmax weights and SiLU gates compare bit for bit. */
+static float exp_rn(float x) {
+    if (x != x) return x;
+    if (x > 89.0f) return INFINITY;
+    if (x < -104.0f) return 0.0f;
+    const double xd = (double)x;
+    const double k = rint(xd * 1.4426950408889634);
+    const double r = (xd - k * 6.93147180369123816490e-01) - k * 1.90821492927058770002e-10;
+    double p = 1.6059043836821614599e-10;      /* 1/13! */
+    p = fma(p, r, 2.0876756987868098979e-09); /* 1/12! */
+    p = fma(p, r, 2.5052108385441718775e-08); /* 1/11! */
+    p = fma(p, r, 2.7557319223985890653e-07); /* 1/10! */
+    p = fma(p, r, 2.7557319223985890653e-06); /* 1/9! */
+    p = fma(p, r, 2.4801587301587301587e-05); /* 1/8! */
+    p = fma(p, r, 1.9841269841269841270e-04); /* 1/7! */
+    p = fma(p, r, 1.3888888888888888889e-03); /* 1/6! */
+    p = fma(p, r, 8.3333333333333333333e-03); /* 1/5! */
+    p = fma(p, r, 4.1666666666666666667e-02); /* 1/4! */
+    p = fma(p, r, 1.6666666666666666667e-01); /* 1/3! */
+    p = fma(p, r, 0.5);
+    p = fma(p, r, 1.0);
+    p = fma(p, r, 1.0);
+    return (float)scalbn(p, (int)k);
+}
+
+/* exp_rn over an array (the oracle's exponential, for the tests). */
+void ndo_exp_rn(const float *x, int n, float *y) {
+    for (int i = 0; i < n; i++) y[i] = exp_rn(x[i]);
+}
 
 static float maxf_cs(float a, float b) { return a > b ? a : (b > a ? b : (a == a ? a : b)); }
 

@@ -10,8 +10,10 @@
  * cited per function (paths are relative to the needle-cs source tree).
  * Floating point follows the reference's scalar C# semantics: IEEE binary32,
  * no FMA contraction (compile with -ffp-contract=off), left-to-right
- * summation, MathF.Exp/Cos/Sin/Pow mapped to the C library's expf/cosf/sinf/
- * powf (which is what .NET calls on Linux).
+ * summation, MathF.Cos/Sin/Pow mapped to the C library's cosf/sinf/powf
+ * (which is what .NET calls on Linux), and MathF.Exp to exp_rn, the float
+ * exponential rounded to nearest, computed from the mathematics with IEEE
+ * double operations (needle_oracle.c).
  */
 #ifndef NEEDLE_ORACLE_H
 #define NEEDLE_ORACLE_H
@@ -32,6 +34,9 @@ void ndo_fill_edges(float *x, int n, uint64_t *state, float scale);
 void ndo_fill_sbyte(int8_t *x, int n, uint64_t *state, int extremes);
 void ndo_fill_bytes(uint8_t *x, int n, uint64_t *state, int extremes);
 uint16_t ndo_half_bits(float value);
+
+/* ---- the exponential (MathF.Exp) over an array ---- */
+void ndo_exp_rn(const float *x, int n, float *y);
 
 /* ---- row primitives (src/Needle/Scalar.cs) ---- */
 float ndo_abs_max(const float *x, int n);

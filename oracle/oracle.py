@@ -32,6 +32,7 @@ _SIGS = {
     "ndo_quantize_rows": (None, [P, I, I, P, P]),
     "ndo_fake_a8": (F, [P, I]),
     "ndo_half_to_single": (F, [_c.c_uint16]),
+    "ndo_exp_rn": (None, [P, I, P]),
     "ndo_hadamard128": (None, [P, P]),
     "ndo_planes": (None, [P, I, P, _c.POINTER(I)]),
     "ndo_sigmoid": (F, [F]),
@@ -135,6 +136,14 @@ class XorShift64:
 
 def f32(a):
     return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def exp_rn(x):
+    """MathF.Exp as the oracle computes it (float in, float out)."""
+    x = f32(x)
+    y = np.empty_like(x)
+    lib().ndo_exp_rn(ptr(x), x.size, ptr(y))
+    return y
 
 
 def quantize_int8(x):

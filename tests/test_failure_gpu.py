@@ -42,3 +42,4 @@ def test_engine_reports_context_exhaustion_without_side_effects(pkg, cuda):
     eng.forward_batch([1, 2], [0, 1], [0, 1])  # and the engine keeps working
     assert eng.slot_length(0) == 61 and eng.slot_length(1) == 1
     eng.close()
+
