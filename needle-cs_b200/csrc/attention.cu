@@ -414,11 +414,16 @@ __device__ __forceinline__ float sum_in_order(const float *s, int n) {
 // One 16-position chunk of pass B for the lane's two dims: va / vb hold the
 // chunk's V bytes of dim lane and lane + 32, w the chunk's 16 weights.
 // Each int8 becomes an exact float through its biased byte (v ^ 0x80 as the
-// low mantissa byte of 2^23), then acc += w * v per position in order.
+// low mantissa byte of 2^23), then acc += w * v per position in order, the
+// product and the sum each rounded.  The product is formed as fma(w, v, -0),
+// which is the rounded product bit for bit (the sign of a zero product
+// included): a separate multiply and add on packed pairs can be contracted
+// into one fused multiply-add by the compiler, which would round once.
 __device__ __forceinline__ uint64_t pv_chunk(uint64_t acc, const uint4 &va, const uint4 &vb, const float *w) {
     const uint32_t wa[4] = {va.x ^ 0x80808080u, va.y ^ 0x80808080u, va.z ^ 0x80808080u, va.w ^ 0x80808080u};
     const uint32_t wb[4] = {vb.x ^ 0x80808080u, vb.y ^ 0x80808080u, vb.z ^ 0x80808080u, vb.w ^ 0x80808080u};
     const uint64_t bias = f2_pack(-8388736.0f, -8388736.0f);  // -(2^23 + 128)
+    const uint64_t neg_zero = f2_pack(-0.0f, -0.0f);
 #pragma unroll
     for (int q = 0; q < 4; q++) {
         const float4 w4 = *reinterpret_cast<const float4 *>(w + 4 * q);
@@ -428,7 +433,7 @@ __device__ __forceinline__ uint64_t pv_chunk(uint64_t acc, const uint4 &va, cons
             const float fa = __uint_as_float(__byte_perm(wa[q], 0x4B000000u, 0x7540u + i));
             const float fb = __uint_as_float(__byte_perm(wb[q], 0x4B000000u, 0x7540u + i));
             const uint64_t v = f2_add(f2_pack(fa, fb), bias);  // exact: both are integers below 2^24
-            acc = f2_add(acc, f2_mul(f2_pack(ww[i], ww[i]), v));
+            acc = f2_add(acc, f2_fma(f2_pack(ww[i], ww[i]), v, neg_zero));
         }
     }
     return acc;
