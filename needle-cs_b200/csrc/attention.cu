@@ -14,8 +14,7 @@
 // (dot * ks) * (qs / sqrt(d)) per position into a shared score buffer.
 // Softmax in the reference's order: max, exp(s - max) per position, their
 // total summed in position order by one lane, each divided by it.  Pass B:
-// out[d] += (p * vs) * v[d] in position order, two dims per lane on packed
-// f32x2 instructions.  Every rounding is the reference's, so the output is
+// out[d] += (p * vs) * v[d] in position order, two dims per lane.  Every rounding is the reference's, so the output is
 // the scalar result exactly (the exponential is the correctly rounded one,
 // exp_rn).  The merge of split partials (MergePartials,
 // src/Needle/Blocks.cs:750-817) is not needed: a row is never split.
@@ -415,15 +414,14 @@ __device__ __forceinline__ float sum_in_order(const float *s, int n) {
 // chunk's V bytes of dim lane and lane + 32, w the chunk's 16 weights.
 // Each int8 becomes an exact float through its biased byte (v ^ 0x80 as the
 // low mantissa byte of 2^23), then acc += w * v per position in order, the
-// product and the sum each rounded.  The product is formed as fma(w, v, -0),
-// which is the rounded product bit for bit (the sign of a zero product
-// included): a separate multiply and add on packed pairs can be contracted
-// into one fused multiply-add by the compiler, which would round once.
-__device__ __forceinline__ uint64_t pv_chunk(uint64_t acc, const uint4 &va, const uint4 &vb, const float *w) {
+// product and the sum each rounded.  They are the scalar __fmul_rn /
+// __fadd_rn, which the compiler never merges into a fused multiply-add (the
+// packed-pair forms, even as fma(w, v, -0), were contracted with the sum).
+__device__ __forceinline__ void pv_chunk(float &acc_a, float &acc_b, const uint4 &va, const uint4 &vb,
+                                         const float *w) {
     const uint32_t wa[4] = {va.x ^ 0x80808080u, va.y ^ 0x80808080u, va.z ^ 0x80808080u, va.w ^ 0x80808080u};
     const uint32_t wb[4] = {vb.x ^ 0x80808080u, vb.y ^ 0x80808080u, vb.z ^ 0x80808080u, vb.w ^ 0x80808080u};
     const uint64_t bias = f2_pack(-8388736.0f, -8388736.0f);  // -(2^23 + 128)
-    const uint64_t neg_zero = f2_pack(-0.0f, -0.0f);
 #pragma unroll
     for (int q = 0; q < 4; q++) {
         const float4 w4 = *reinterpret_cast<const float4 *>(w + 4 * q);
@@ -432,11 +430,12 @@ __device__ __forceinline__ uint64_t pv_chunk(uint64_t acc, const uint4 &va, cons
         for (int i = 0; i < 4; i++) {
             const float fa = __uint_as_float(__byte_perm(wa[q], 0x4B000000u, 0x7540u + i));
             const float fb = __uint_as_float(__byte_perm(wb[q], 0x4B000000u, 0x7540u + i));
-            const uint64_t v = f2_add(f2_pack(fa, fb), bias);  // exact: both are integers below 2^24
-            acc = f2_add(acc, f2_fma(f2_pack(ww[i], ww[i]), v, neg_zero));
+            float va_f, vb_f;
+            f2_unpack(f2_add(f2_pack(fa, fb), bias), va_f, vb_f);  // exact: both are integers below 2^24
+            acc_a = __fadd_rn(acc_a, __fmul_rn(ww[i], va_f));
+            acc_b = __fadd_rn(acc_b, __fmul_rn(ww[i], vb_f));
         }
     }
-    return acc;
 }
 
 __device__ __forceinline__ void attn_consumer(const AttnArgs &a, const AttnSmem &L, uint8_t *smem, uint64_t *full,
@@ -516,7 +515,7 @@ __device__ __forceinline__ void attn_consumer(const AttnArgs &a, const AttnSmem 
         for (int j = lane; j < len; j += 32) sc[j] = __fdiv_rn(sc[j], total);
         __syncwarp();
         // ---- pass B: out[d] += (p_j * vs_j) * v_j[d] in position order ----
-        uint64_t acc = f2_pack(0.0f, 0.0f);  // dims lane, lane + 32
+        float acc_a = 0.0f, acc_b = 0.0f;  // dims lane, lane + 32
         for (int pg = 0; pg < n_pages; pg++) {
             const int stage = consumed % kAttnStages;
             if (!mbar_wait_bounded(&f_bar[stage], (consumed / kAttnStages) & 1, kWaitLimit)) {
@@ -540,12 +539,11 @@ __device__ __forceinline__ void attn_consumer(const AttnArgs &a, const AttnSmem 
             if (lane == 0) mbar_arrive(&e_bar[stage]);
             consumed++;
 #pragma unroll
-            for (int ch = 0; ch < 4; ch++) acc = pv_chunk(acc, va[ch], vb[ch], wbuf + 16 * ch);
+            for (int ch = 0; ch < 4; ch++) pv_chunk(acc_a, acc_b, va[ch], vb[ch], wbuf + 16 * ch);
             __syncwarp();  // the weights are read before the next page rewrites them
         }
         if (timed_out) break;
-        float o0, o1;
-        f2_unpack(acc, o0, o1);
+        float o0 = acc_a, o1 = acc_b;
         if (poisoned) o0 = o1 = __int_as_float(0x7fc00000);
         float *out = a.out + ((size_t)row * a.heads + head) * kHeadDim;
         out[lane] = o0;
