@@ -8,8 +8,8 @@
 // Decode attention, bit for bit Scalar.AttentionHead (src/Needle/Scalar.cs:
 // 290-312) over the whole row: persistent warps stream (row, head) items from
 // a work list built once per step.  Each page's (layer, head) record arrives
-// in shared memory as two bulk copies (K half, V half), issued by a producer
-// warp into a ring per consumer warp (mbarrier completion, bounded waits).
+// in shared memory as two bulk copies (K half, V half) that the warp issues
+// into its own ring (mbarrier completion, bounded waits).
 // Pass A: the int8 dots on tensor cores (mma.sync s8, exact int32), then
 // (dot * ks) * (qs / sqrt(d)) per position into a shared score buffer.
 // Softmax in the reference's order: max, exp(s - max) per position, their
@@ -181,38 +181,26 @@ int launch_cross_kv_write(const float *y, int frames, int heads, const int32_t *
 }
 
 // ------------------------------------------------------ decode attention --
-constexpr int kAttnConsumers = 4;  // consumer warps per CTA; warp 4 is the producer
-constexpr int kAttnStages = 4;     // ring stages (half records) per consumer
-constexpr int kAttnThreads = 32 * (kAttnConsumers + 1);
-// Per-stage header, written by the producer: with an item's first copy
-// {row, head, len, pages} (row -1 = the list ended), the query scale at byte
-// 16 and the 64 query bytes at byte 32; with every copy the int at byte 24:
-// 1 if the page was copied, 0 if its id was outside the pool (the stage then
-// holds stale bytes and the item's output becomes NaN).
-constexpr int kAttnHdrBytes = 96;
-// A producer lane reads the result of its item claim (an atomic) and of a
-// query-scale load only this many SM cycles after issuing them, so the
-// warp's other lanes are not held on the load's scoreboard.
-constexpr long long kAttnLatencyCycles = 1000;
+constexpr int kAttnWarps = 4;   // warps per CTA; each works its own items
+constexpr int kAttnStages = 3;  // ring stages (half records) per warp
+constexpr int kAttnThreads = 32 * kAttnWarps;
+constexpr int kAttnPageRegs = kAttnMaxPositions / kPagePositions / 32;  // page ids per lane of an item
 constexpr uint32_t kWaitLimit = 1u << 22;
-constexpr uint32_t kPollLimit = 1u << 24;  // producer polls without progress (with a short sleep each)
 
-// Shared memory of one CTA for rows of at most max_pages pages: per consumer
-// [ring stages][stage headers][64 PV weights][2 work records][scores], then
-// the barriers full[consumer][stage], empty[consumer][stage], record[consumer].
+// Shared memory of one CTA for rows of at most max_pages pages: per warp
+// [ring stages][64 PV weights][stage page flags][scores], then the
+// barriers full[warp][stage].
 struct AttnSmem {
-    int record_bytes, hdr, wbuf, rec, scores, consumer, bars, total;
+    int wbuf, flags, scores, warp_bytes, bars, total;
 };
 __host__ __device__ __forceinline__ AttnSmem attn_smem(int max_pages) {
     AttnSmem s;
-    s.record_bytes = attn_record_ints(max_pages) * 4;
-    s.hdr = kAttnStages * kKvHalfBytes;
-    s.wbuf = s.hdr + kAttnStages * kAttnHdrBytes;
-    s.rec = s.wbuf + kPagePositions * 4;
-    s.scores = s.rec + 2 * s.record_bytes;
-    s.consumer = s.scores + max_pages * kPagePositions * 4;
-    s.bars = kAttnConsumers * s.consumer;
-    s.total = s.bars + (2 * kAttnStages + 1) * kAttnConsumers * 8;
+    s.wbuf = kAttnStages * kKvHalfBytes;
+    s.flags = s.wbuf + kPagePositions * 4;
+    s.scores = s.flags + 16;
+    s.warp_bytes = s.scores + max_pages * kPagePositions * 4;
+    s.bars = kAttnWarps * s.warp_bytes;
+    s.total = s.bars + kAttnWarps * kAttnStages * 8;
     return s;
 }
 
@@ -249,150 +237,6 @@ __global__ void __launch_bounds__(128) attn_work_kernel(AttnArgs a) {
     if (!valid)
         for (int t = threadIdx.x; t < a.heads * kHeadDim; t += blockDim.x)
             a.out[(size_t)row * a.heads * kHeadDim + t] = __int_as_float(0x7fc00000);
-}
-
-// Persistent, warp-specialised.  Items are (row position, head) with heads
-// innermost, rows longest first; consumer warp w takes item w first, after
-// that its producer lane claims the next unclaimed item from a counter in
-// global memory whenever it starts issuing the current one, so warps that
-// stream slower take fewer items and the launch's warps finish together.
-// Lane c of the producer warp feeds consumer c through a small state machine
-// so that no lane's latency holds the warp: claim (atomic; read
-// kAttnLatencyCycles later), fetch the item's row record with its page ids
-// into shared memory (cp.async.bulk, double-buffered, polled on its own
-// mbarrier), load the query scale (read kAttnLatencyCycles later).  Per item
-// it issues 2 * pages copies into the consumer's ring: every page's K half,
-// then every page's V half; with the first it writes the item header and
-// copies the 64 query bytes beside it.  Every wait and poll is bounded.
-__device__ __forceinline__ void attn_producer(const AttnArgs &a, const AttnSmem &L, uint8_t *smem, uint64_t *full,
-                                              uint64_t *empty, uint64_t *record_bar, int lane) {
-    const int W = gridDim.x * kAttnConsumers;
-    const int c = lane;
-    const int n_work = a.n_work[0];
-    int *next_item = a.n_work + 1;
-    const int rec_ints = L.record_bytes / 4;
-    enum { kClaimed, kFetching, kScale, kReady, kExhausted };
-    bool done = c >= kAttnConsumers, ending = false;
-    uint8_t *base = smem + (size_t)(done ? 0 : c) * L.consumer;
-    int fs = kClaimed, claim = blockIdx.x * kAttnConsumers + c;  // the first item is this warp's own
-    int nx_buf = 0, cur_buf = 1;
-    int nx_row = 0, nx_head = 0, nx_len = 0, nx_pages = 0;
-    int cur_row = 0, cur_head = 0, cur_len = 0, cur_pages = 0;
-    float qs_nx = 0.0f, qs_cur = 0.0f;
-    long long t_issue = clock64() - kAttnLatencyCycles;
-    unsigned fetches = 0, issued = 0;
-    int k = 0;  // next copy of the current item: K halves 0..pages-1, then V halves
-    uint32_t idle = 0;
-    bool timed_out = false;
-    while (true) {
-        bool send = false;
-        int stage = 0;
-        if (!done) {
-            // one step of the next item's fetch
-            if (fs == kClaimed && clock64() - t_issue >= kAttnLatencyCycles) {
-                if (claim < n_work) {
-                    nx_head = claim % a.heads;
-                    fence_proxy_async_smem();
-                    mbar_arrive_expect_tx(&record_bar[c], (uint32_t)L.record_bytes);
-                    bulk_g2s(base + L.rec + nx_buf * L.record_bytes, a.work + (size_t)(claim / a.heads) * rec_ints,
-                             (uint32_t)L.record_bytes, &record_bar[c]);
-                    fs = kFetching;
-                } else {
-                    fs = kExhausted;
-                }
-            } else if (fs == kFetching && mbar_test_wait(&record_bar[c], fetches & 1)) {
-                fetches++;
-                const int4 h = *reinterpret_cast<const int4 *>(base + L.rec + nx_buf * L.record_bytes);
-                nx_row = h.x;
-                nx_len = h.y;
-                nx_pages = h.w;
-                t_issue = clock64();
-                if (nx_pages == 0) {  // an out-of-range row: nothing to attend, take another item
-                    claim = W + atomicAdd(next_item, 1);
-                    fs = kClaimed;
-                } else {
-                    qs_nx = __ldg(a.qs + (size_t)nx_row * a.heads + nx_head);
-                    fs = kScale;
-                }
-            } else if (fs == kScale && clock64() - t_issue >= kAttnLatencyCycles) {
-                fs = kReady;
-            }
-            // the next item starts once the current one is issued
-            if (!ending && k == 2 * cur_pages) {
-                if (fs == kReady) {
-                    cur_row = nx_row, cur_head = nx_head, cur_len = nx_len, cur_pages = nx_pages;
-                    qs_cur = qs_nx;
-                    cur_buf = nx_buf;
-                    nx_buf ^= 1;
-                    k = 0;
-                    claim = W + atomicAdd(next_item, 1);
-                    t_issue = clock64();
-                    fs = kClaimed;
-                } else if (fs == kExhausted) {
-                    ending = true;
-                }
-            }
-            if (ending || k < 2 * cur_pages) {
-                stage = issued % kAttnStages;
-                send = issued < (unsigned)kAttnStages ||
-                       mbar_test_wait(&empty[c * kAttnStages + stage], ((issued / kAttnStages) - 1) & 1);
-            }
-        }
-        if (send) {  // lanes with a free stage issue together
-            uint64_t *bar = &full[c * kAttnStages + stage];
-            uint8_t *hdr = base + L.hdr + stage * kAttnHdrBytes;
-            if (ending) {  // end marker: no copy, the consumer reads row -1 and stops
-                *reinterpret_cast<int4 *>(hdr) = make_int4(-1, 0, 0, 0);
-                mbar_arrive(bar);
-                done = true;
-            } else {
-                const bool first = k == 0;
-                const bool v_half = k >= cur_pages;
-                const int pi = v_half ? k - cur_pages : k;
-                const int page = reinterpret_cast<const int *>(base + L.rec + cur_buf * L.record_bytes)[4 + pi];
-                k++;
-                const bool page_ok = page >= 0 && page < a.num_pages;
-                if (!page_ok && a.status) atomicOr(a.status, kStatusBadPage);
-                if (first) {
-                    *reinterpret_cast<int4 *>(hdr) = make_int4(cur_row, cur_head, cur_len, cur_pages);
-                    *reinterpret_cast<float *>(hdr + 16) = qs_cur;
-                }
-                *reinterpret_cast<int *>(hdr + 24) = page_ok ? 1 : 0;
-                const uint32_t tx = (page_ok ? kKvHalfBytes : 0) + (first ? kHeadDim : 0);
-                if (tx == 0) {
-                    mbar_arrive(bar);
-                } else {
-                    fence_proxy_async_smem();
-                    mbar_arrive_expect_tx(bar, tx);
-                    if (page_ok)
-                        bulk_g2s(base + stage * kKvHalfBytes,
-                                 a.pool + (size_t)page * a.page_bytes + kv_block_offset(a.layer, cur_head, a.heads) +
-                                     (v_half ? kKvHalfBytes : 0),
-                                 kKvHalfBytes, bar);
-                    if (first)
-                        bulk_g2s(hdr + 32, a.q + ((size_t)cur_row * a.heads + cur_head) * kHeadDim, kHeadDim, bar);
-                }
-            }
-            issued++;
-        }
-        const unsigned busy = __ballot_sync(0xffffffffu, !done), moved = __ballot_sync(0xffffffffu, send);
-        if (!busy) break;
-        if (moved) {
-            idle = 0;
-        } else if (++idle > kPollLimit) {
-            timed_out = true;
-            break;
-        } else {
-            __nanosleep(64);
-        }
-    }
-    if (timed_out && lane == 0 && a.status) atomicOr(a.status, kStatusTimeout);
-    // drain: every copy this lane issued lands before the CTA exits (bounded)
-    if (c < kAttnConsumers) {
-        if (fs == kFetching) mbar_wait_bounded(&record_bar[c], fetches & 1, kWaitLimit);
-        for (unsigned j = issued > (unsigned)kAttnStages ? issued - kAttnStages : 0u; j < issued; j++)
-            mbar_wait_bounded(&full[c * kAttnStages + j % kAttnStages], (j / kAttnStages) & 1, kWaitLimit);
-    }
 }
 
 // Sum of s[0..n) in position order (one lane: the reference's loop).
@@ -438,41 +282,161 @@ __device__ __forceinline__ void pv_chunk(float &acc_a, float &acc_b, const uint4
     }
 }
 
-__device__ __forceinline__ void attn_consumer(const AttnArgs &a, const AttnSmem &L, uint8_t *smem, uint64_t *full,
-                                              uint64_t *empty, int warp, int lane) {
+// One (row, head) item as a warp holds it in registers: its work record
+// (row, attended positions, page count; lane l keeps page ids l, l+32, ...)
+// and, once fetched, the query scale and the lane's 16 query bytes.
+struct AttnItemRegs {
+    int item, row, head, len, pages;
+    int page[kAttnPageRegs];
+    float qs;
+    uint4 q;
+};
+
+// The record of `item` (no use of the result yet: the loads stay in flight).
+__device__ __forceinline__ void item_fetch_record(const AttnArgs &a, int item, int n_work, int lane,
+                                                  AttnItemRegs &it) {
+    it.item = item;
+    it.pages = 0;
+    if (item >= n_work) return;
+    const int32_t *rec = a.work + (size_t)(item / a.heads) * attn_record_ints(a.max_pages);
+    const int4 h = __ldg(reinterpret_cast<const int4 *>(rec));
+    it.head = item % a.heads;
+    it.row = h.x;
+    it.len = h.y;
+    it.pages = h.w;
+#pragma unroll
+    for (int j = 0; j < kAttnPageRegs; j++) {
+        const int idx = lane + 32 * j;
+        it.page[j] = idx < a.max_pages ? __ldg(rec + 4 + idx) : -1;
+    }
+}
+// The item's query scale and the lane's query chunk (k_slot chunk tig).
+__device__ __forceinline__ void item_fetch_query(const AttnArgs &a, int lane, AttnItemRegs &it) {
+    if (it.pages == 0) return;
+    const size_t rh = (size_t)it.row * a.heads + it.head;
+    it.qs = __ldg(a.qs + rh);
+    it.q = __ldg(reinterpret_cast<const uint4 *>(a.q + rh * kHeadDim) + (lane & 3));
+}
+__device__ __forceinline__ int item_page(const AttnItemRegs &it, int pi) {
+    const int j = pi >> 5;
+    int v = it.page[0];
+#pragma unroll
+    for (int r = 1; r < kAttnPageRegs; r++)
+        if (j == r) v = it.page[r];
+    return __shfl_sync(0xffffffffu, v, pi & 31);
+}
+
+// A warp's copy stream: every item's K halves, then its V halves, into the
+// warp's ring.  Copies of the current item go out first; those of the next
+// item once its record is in registers (`next_ready`), so item boundaries
+// overlap.  Lane 0 issues; all lanes keep the counters.
+struct AttnStream {
+    unsigned issued, consumed;
+    int k_cur, k_next;
+};
+__device__ __forceinline__ void attn_issue(const AttnArgs &a, uint8_t *wsm, int *flags, uint64_t *full,
+                                           AttnStream &st, const AttnItemRegs &cur, const AttnItemRegs &nx,
+                                           bool next_ready, int lane) {
+    while (st.issued - st.consumed < (unsigned)kAttnStages) {
+        const bool use_cur = st.k_cur < 2 * cur.pages;  // lane-uniform
+        if (!use_cur && !(next_ready && st.k_next < 2 * nx.pages)) break;
+        const int k = use_cur ? st.k_cur++ : st.k_next++;
+        const int pages = use_cur ? cur.pages : nx.pages, head = use_cur ? cur.head : nx.head;
+        const bool v_half = k >= pages;
+        const int pi = v_half ? k - pages : k;
+        const int page = use_cur ? item_page(cur, pi) : item_page(nx, pi);
+        const int stage = st.issued % kAttnStages;
+        if (lane == 0) {
+            const bool ok = page >= 0 && page < a.num_pages;
+            flags[stage] = ok ? 1 : 0;
+            if (!ok) {
+                if (a.status) atomicOr(a.status, kStatusBadPage);
+                mbar_arrive(&full[stage]);  // completes the phase without a copy; the stage holds stale bytes
+            } else {
+                fence_proxy_async_smem();
+                mbar_arrive_expect_tx(&full[stage], kKvHalfBytes);
+                bulk_g2s(wsm + stage * kKvHalfBytes,
+                         a.pool + (size_t)page * a.page_bytes + kv_block_offset(a.layer, head, a.heads) +
+                             (v_half ? kKvHalfBytes : 0),
+                         kKvHalfBytes, &full[stage]);
+            }
+        }
+        st.issued++;
+    }
+}
+
+// Persistent warps, each working (row position, head) items of the work list
+// (rows longest first, heads innermost): warp w of the grid takes item w
+// first, then claims the next unclaimed item from a counter in global memory
+// one item ahead, so warps that stream slower take fewer items and the
+// launch's warps finish together.  Per item the warp streams 2 * pages half
+// records through its 3-stage ring (cp.async.bulk, mbarrier completion,
+// bounded waits), every page's K half, then every page's V half:
+//  * pass A: the page's K fragments to registers, exact int32 dots on tensor
+//    cores (mma.sync m16n8k32 s8, K as A, the query in every B column; lane
+//    (gid, tig) keeps positions 16*tig + gid and + 8), then
+//    s = (dot * ks) * (qs / sqrt(d)) into the warp's score buffer;
+//  * softmax as Scalar.Softmax: max, e = exp_rn(s - max) per position, their
+//    total summed in position order by one lane, p = e / total;
+//  * pass B: weights w = p * vs per position, then out[d] += w * v[d] in
+//    position order, two dims (lane, lane + 32) per lane.
+// The next item's claim, record and query are loaded into registers while
+// the current one computes, each used only a phase after its load was issued.
+__global__ void __launch_bounds__(kAttnThreads, 3) attn_decode_kernel(AttnArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const AttnSmem L = attn_smem(a.max_pages);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int gid = lane >> 2, tig = lane & 3;
-    uint8_t *base = smem + (size_t)warp * L.consumer;
-    const uint8_t *headers = base + L.hdr;
-    float *wbuf = reinterpret_cast<float *>(base + L.wbuf);
-    float *sc = reinterpret_cast<float *>(base + L.scores);
-    uint64_t *f_bar = full + warp * kAttnStages, *e_bar = empty + warp * kAttnStages;
+    uint8_t *wsm = smem + (size_t)warp * L.warp_bytes;
+    float *wbuf = reinterpret_cast<float *>(wsm + L.wbuf);
+    int *flags = reinterpret_cast<int *>(wsm + L.flags);
+    float *sc = reinterpret_cast<float *>(wsm + L.scores);
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + L.bars) + warp * kAttnStages;
+    if (lane == 0) {
+        for (int i = 0; i < kAttnStages; i++) mbar_init(&full[i], 1);
+        fence_mbar_init();
+    }
+    __syncwarp();
+    pdl_wait();
+    pdl_trigger();
+    const int n_work = a.n_work[0];
+    int *next_item = a.n_work + 1;
+    const int W = gridDim.x * kAttnWarps;
     const int p0 = 16 * tig + gid, p1 = p0 + 8;  // the positions of this lane's two QK results
     const int swz = (lane >> 1) & 3;             // V chunk rotation of dims lane and lane + 32
-    unsigned consumed = 0;
+    AttnStream st{0u, 0u, 0, 0};
+    AttnItemRegs cur, nx;
+    item_fetch_record(a, blockIdx.x * kAttnWarps + warp, n_work, lane, cur);
+    item_fetch_query(a, lane, cur);
+    nx.item = n_work;
+    nx.pages = 0;
     bool timed_out = false;
-    while (!timed_out) {
-        // the item's first stage carries its header (or the end marker)
-        const int stage0 = consumed % kAttnStages;
-        if (!mbar_wait_bounded(&f_bar[stage0], (consumed / kAttnStages) & 1, kWaitLimit)) {
-            timed_out = true;
-            break;
+    while (cur.item < n_work && !timed_out) {
+        if (cur.pages == 0) {  // an out-of-range row: nothing to attend (its outputs are NaN already)
+            int claim = 0;
+            if (lane == 0) claim = W + atomicAdd(next_item, 1);
+            item_fetch_record(a, __shfl_sync(0xffffffffu, claim, 0), n_work, lane, cur);
+            item_fetch_query(a, lane, cur);
+            st.k_cur = 0;
+            continue;
         }
-        const uint8_t *hdr = headers + stage0 * kAttnHdrBytes;
-        const int4 meta = *reinterpret_cast<const int4 *>(hdr);
-        if (meta.x < 0) break;  // the list ended for this warp
-        const uint4 qv = *reinterpret_cast<const uint4 *>(hdr + 32 + tig * 16);  // K-dim chunk tig, both k-steps
-        const float scale = __fmul_rn(*reinterpret_cast<const float *>(hdr + 16), a.inv_sqrt_d);
-        const int row = meta.x, head = meta.y, len = meta.z, n_pages = meta.w;
+        int claim = 0;
+        if (lane == 0) claim = W + atomicAdd(next_item, 1);  // the next item, read after pass A
+        bool next_ready = false;
+        attn_issue(a, wsm, flags, full, st, cur, nx, next_ready, lane);
+        const float scale = __fmul_rn(cur.qs, a.inv_sqrt_d);
+        const uint4 qv = cur.q;
+        const int len = cur.len, n_pages = cur.pages;
         bool poisoned = false;
         float peak = -INFINITY;
         // ---- pass A: s_j = (dot_j * ks_j) * scale for every position ----
         for (int pg = 0; pg < n_pages; pg++) {
-            const int stage = consumed % kAttnStages;
-            if (pg > 0 && !mbar_wait_bounded(&f_bar[stage], (consumed / kAttnStages) & 1, kWaitLimit)) {
+            const int stage = st.consumed % kAttnStages;
+            if (!mbar_wait_bounded(&full[stage], (st.consumed / kAttnStages) & 1, kWaitLimit)) {
                 timed_out = true;
                 break;
             }
-            const uint8_t *blk = base + stage * kKvHalfBytes;
+            const uint8_t *blk = wsm + stage * kKvHalfBytes;
             uint4 kf[4][2];
 #pragma unroll
             for (int mt = 0; mt < 4; mt++) {
@@ -480,10 +444,11 @@ __device__ __forceinline__ void attn_consumer(const AttnArgs &a, const AttnSmem 
                 kf[mt][1] = *reinterpret_cast<const uint4 *>(blk + mt * 1024 + 512 + lane * 16);
             }
             const float2 ks = *reinterpret_cast<const float2 *>(blk + kKScaleOffset + 8 * lane);
-            if (!*reinterpret_cast<const int *>(headers + stage * kAttnHdrBytes + 24)) poisoned = true;
+            if (!flags[stage]) poisoned = true;
+            fence_proxy_async_smem();  // these reads before the stage's next copy
             __syncwarp();
-            if (lane == 0) mbar_arrive(&e_bar[stage]);
-            consumed++;
+            st.consumed++;
+            attn_issue(a, wsm, flags, full, st, cur, nx, next_ready, lane);
             int dot0 = 0, dot1 = 0;
 #pragma unroll
             for (int mt = 0; mt < 4; mt++) {
@@ -505,6 +470,8 @@ __device__ __forceinline__ void attn_consumer(const AttnArgs &a, const AttnSmem 
             }
         }
         if (timed_out) break;
+        // the next item's record (the claim has long returned)
+        item_fetch_record(a, __shfl_sync(0xffffffffu, claim, 0), n_work, lane, nx);
         // ---- softmax (Scalar.Softmax): exp(s - peak), total in position order, p = e / total ----
         peak = warp_max_f(peak);
         __syncwarp();
@@ -514,15 +481,17 @@ __device__ __forceinline__ void attn_consumer(const AttnArgs &a, const AttnSmem 
         total = __shfl_sync(0xffffffffu, total, 0);
         for (int j = lane; j < len; j += 32) sc[j] = __fdiv_rn(sc[j], total);
         __syncwarp();
+        item_fetch_query(a, lane, nx);
+        next_ready = true;
         // ---- pass B: out[d] += (p_j * vs_j) * v_j[d] in position order ----
         float acc_a = 0.0f, acc_b = 0.0f;  // dims lane, lane + 32
         for (int pg = 0; pg < n_pages; pg++) {
-            const int stage = consumed % kAttnStages;
-            if (!mbar_wait_bounded(&f_bar[stage], (consumed / kAttnStages) & 1, kWaitLimit)) {
+            const int stage = st.consumed % kAttnStages;
+            if (!mbar_wait_bounded(&full[stage], (st.consumed / kAttnStages) & 1, kWaitLimit)) {
                 timed_out = true;
                 break;
             }
-            const uint8_t *blk = base + stage * kKvHalfBytes;  // [V scales][V dim-major]
+            const uint8_t *blk = wsm + stage * kKvHalfBytes;  // [V scales][V dim-major]
             const float *vs = reinterpret_cast<const float *>(blk);
             const int valid = min(kPagePositions, len - pg * kPagePositions);
             // positions past the row's end get weight 0: 0 * v adds a zero, which leaves acc unchanged
@@ -534,45 +503,34 @@ __device__ __forceinline__ void attn_consumer(const AttnArgs &a, const AttnSmem 
                 va[ch] = *reinterpret_cast<const uint4 *>(blk + 256 + lane * 64 + ((ch ^ swz) << 4));
                 vb[ch] = *reinterpret_cast<const uint4 *>(blk + 256 + (lane + 32) * 64 + ((ch ^ swz) << 4));
             }
-            if (!*reinterpret_cast<const int *>(headers + stage * kAttnHdrBytes + 24)) poisoned = true;
+            if (!flags[stage]) poisoned = true;
+            fence_proxy_async_smem();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&e_bar[stage]);
-            consumed++;
+            st.consumed++;
+            attn_issue(a, wsm, flags, full, st, cur, nx, next_ready, lane);
 #pragma unroll
             for (int ch = 0; ch < 4; ch++) pv_chunk(acc_a, acc_b, va[ch], vb[ch], wbuf + 16 * ch);
             __syncwarp();  // the weights are read before the next page rewrites them
         }
         if (timed_out) break;
-        float o0 = acc_a, o1 = acc_b;
-        if (poisoned) o0 = o1 = __int_as_float(0x7fc00000);
-        float *out = a.out + ((size_t)row * a.heads + head) * kHeadDim;
-        out[lane] = o0;
-        out[lane + 32] = o1;
+        float *out = a.out + ((size_t)cur.row * a.heads + cur.head) * kHeadDim;
+        const float nan = __int_as_float(0x7fc00000);
+        out[lane] = poisoned ? nan : acc_a;
+        out[lane + 32] = poisoned ? nan : acc_b;
+        // the next item becomes current, with the copies already issued for it
+        cur = nx;
+        st.k_cur = st.k_next;
+        st.k_next = 0;
+        nx.item = n_work;
+        nx.pages = 0;
     }
-    if (timed_out && lane == 0 && a.status) atomicOr(a.status, kStatusTimeout);
-}
-
-__global__ void __launch_bounds__(kAttnThreads, 2) attn_decode_kernel(AttnArgs a) {
-    extern __shared__ __align__(128) uint8_t smem[];
-    const AttnSmem L = attn_smem(a.max_pages);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem + L.bars);  // [consumer][stage]
-    uint64_t *empty = full + kAttnConsumers * kAttnStages;
-    uint64_t *record_bar = empty + kAttnConsumers * kAttnStages;  // [consumer]
-    if (threadIdx.x == 0) {
-        for (int i = 0; i < kAttnConsumers * kAttnStages; i++) mbar_init(&full[i], 1), mbar_init(&empty[i], 1);
-        for (int i = 0; i < kAttnConsumers; i++) mbar_init(&record_bar[i], 1);
-        fence_mbar_init();
+    if (timed_out) {
+        if (lane == 0 && a.status) atomicOr(a.status, kStatusTimeout);
+        // every copy in flight lands before the warp exits (bounded)
+        for (unsigned j = st.consumed; j < st.issued; j++)
+            mbar_wait_bounded(&full[j % kAttnStages], (j / kAttnStages) & 1, kWaitLimit);
     }
-    __syncthreads();
-    pdl_wait();
-    pdl_trigger();
-    if (warp == kAttnConsumers)
-        attn_producer(a, L, smem, full, empty, record_bar, lane);
-    else
-        attn_consumer(a, L, smem, full, empty, warp, lane);
-    // every producer lane has taken its last item: the last CTA out resets
-    // the item counter and the finish count for the next launch
+    // the last CTA out resets the item counter and the finish count for the next launch
     __syncthreads();
     if (threadIdx.x == 0) {
         __threadfence();
@@ -666,7 +624,7 @@ int launch_attn_decode(const AttnArgs &a, cudaStream_t stream, bool build_work, 
         int st = launch_attn_work(a, stream);
         if (st != NDL_OK) return st;
     }
-    long long blocks = (items + kAttnConsumers - 1) / kAttnConsumers;
+    long long blocks = (items + kAttnWarps - 1) / kAttnWarps;
     const long long resident = (long long)device_sm_count() * attn_ctas_per_sm(smem);
     if (blocks > resident) blocks = resident;
     launch_kernel(attn_decode_kernel, dim3((unsigned)blocks), dim3(kAttnThreads), smem, stream, a);

@@ -66,27 +66,6 @@ def read_slot_kv(engine, slot, positions):
     return out
 
 
-def logits_close(got, ref, atol=1e-3, rtol=1e-2):
-    """BASELINE tolerance for logits: max-abs 1e-3 or rel 1e-2 per element."""
-    err = np.abs(got - ref)
-    return bool(np.all((err <= atol) | (err <= rtol * np.abs(ref)))), float(err.max())
-
-
-def logits_parity(got, ref, atol=1e-3, rtol=1e-2):
-    """Per element within max-abs 1e-3 or rel 1e-2, or else the reference's
-    own logits criterion (tests/Needle.Tests/ParityTests.cs:47-59): cosine
-    similarity above 0.99995 with the same argmax.  The second form covers a
-    row where one int8 quantization step rounded the other way (a value within
-    an ulp of a rounding boundary: the attention sums are not bit-identical),
-    which moves many head logits by a few 1e-3 at once."""
-    ok, err = logits_close(got, ref, atol, rtol)
-    if ok:
-        return True, err
-    g, r = got.astype(np.float64), ref.astype(np.float64)
-    cos = float(g @ r / (np.linalg.norm(g) * np.linalg.norm(r)))
-    return cos > 0.99995 and int(np.argmax(got)) == int(np.argmax(ref)), err
-
-
 def top2_margin(x):
     s = np.sort(x)
     return float(s[-1] - s[-2])
@@ -118,35 +97,3 @@ def oracle_greedy(ops, oracle, dec, seed, session, length, token, steps):
         ids.append(token)
         pos += 1
     return ids, logits
-
-
-class ParityTally:
-    """Logits of (row, step) pairs against the oracle: strict when every
-    element is within max-abs 1e-3 or rel 1e-2; otherwise the reference's
-    ParityTests criterion must hold (cosine > 0.99995, same argmax), and the
-    oracle's top-2 margin must exceed ten times the largest element error so
-    that the shared argmax is not decided by the difference."""
-
-    def __init__(self):
-        self.total = 0
-        self.strict = 0
-        self.fallback = []  # (label, max err, oracle top-2 margin, cosine)
-        self.worst = 0.0
-
-    def add(self, label, got, ref):
-        self.total += 1
-        ok, err = logits_close(got, ref)
-        self.worst = max(self.worst, err)
-        if ok:
-            self.strict += 1
-            return
-        g, r = got.astype(np.float64), ref.astype(np.float64)
-        cos = float(g @ r / (np.linalg.norm(g) * np.linalg.norm(r)))
-        margin = top2_margin(ref)
-        self.fallback.append((label, err, margin, cos))
-        assert cos > 0.99995 and int(np.argmax(got)) == int(np.argmax(ref)), (label, err, cos)
-        assert margin > 10 * err, (label, err, margin)
-
-    def summary(self):
-        return (f"{self.total} logit rows: {self.strict} within max-abs 1e-3 / rel 1e-2, "
-                f"{len(self.fallback)} by the cosine criterion; largest element error {self.worst:.2e}")

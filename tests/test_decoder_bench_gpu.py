@@ -8,15 +8,15 @@ model seed 1) in the two shapes the benchmark measures:
 Sessions, lengths and first tokens are drawn exactly as bench.py draws them.
 Every step feeds each row's greedy id back, 16 steps in a row.  Bars: the
 token ids of every checked session are identical to the oracle's at every
-step (ParityTests.cs:80-100 greedy generation); every logit row is within
-max-abs 1e-3 / rel 1e-2 per element, or else meets the reference's own
-criterion (cosine > 0.99995, same argmax) with an oracle top-2 margin above
-ten times its largest error.  The count of such rows is printed.
+step (ParityTests.cs:80-100 greedy generation) and every logit is
+bit-identical to the oracle's (BASELINE's bar is max-abs 1e-3 / rel 1e-2;
+each kernel of the step keeps the reference's rounding order, so the
+12-layer chain does not drift at all).
 """
 import numpy as np
 import pytest
 
-from decoder_support import ParityTally, oracle_decoder, oracle_greedy, parallel_map
+from decoder_support import oracle_decoder, oracle_greedy, parallel_map
 
 pytestmark = pytest.mark.gpu
 
@@ -65,11 +65,8 @@ def test_benchmark_decoder_greedy_matches_oracle(pkg, ops, oracle, cuda, preset)
         return oracle_greedy(ops, oracle, dec, p["seed"], r, int(lengths[r]), int(tokens[r]), STEPS)
 
     results = parallel_map(replay, checked)
-    tally = ParityTally()
     for r, (ids, logits) in zip(checked, results):
-        for s in range(STEPS):
-            tally.add((r, s), gpu_logits[r][s], logits[s])
         assert list(gpu_ids[:, r]) == ids, (r, list(gpu_ids[:, r]), ids)
-    print(f"\n{preset}: {len(checked)} sessions x {STEPS} greedy steps, ids identical; {tally.summary()}")
-    for label, err, margin, cos in tally.fallback:
-        print(f"  row {label}: max err {err:.2e}, oracle top-2 margin {margin:.3f}, cosine {cos:.7f}")
+        for s in range(STEPS):
+            got, ref = gpu_logits[r][s], logits[s]
+            assert np.array_equal(got, ref), (r, s, float(np.abs(got - ref).max()))
