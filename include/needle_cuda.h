@@ -68,9 +68,9 @@ enum {
  * timeout and returns.  Returns NDL_ERR_TIMEOUT, the status every kernel
  * reports after a wait that ran out; the context stays usable. */
 NDL_API int ndl_selftest_bounded_wait(int tests);
-/* The library's float exponential (MathF.Exp as its softmax and SiLU
- * compute it) over n device floats, on `stream`: for pinning it to a CPU
- * restatement.  No counterpart in the reference. */
+/* The library's float exponential (the reference's Ops.Exp, which its
+ * softmax and SiLU use) over n device floats, on `stream`: for pinning it to
+ * a CPU restatement.  No counterpart in the reference. */
 NDL_API int ndl_selftest_exp(const float *x, int n, float *y, void *stream);
 
 /* Library identity and diagnostics (no reference counterpart). */

@@ -5,19 +5,19 @@
 // then QuantizeInt8 of q per head and of k, v per (position, head) into the
 // slot's page.  Bit-exact: round-to-nearest products, no FMA.
 //
-// Decode attention, bit for bit Scalar.AttentionHead (src/Needle/Scalar.cs:
-// 290-312) over the whole row: persistent warps stream (row, head) items from
-// a work list built once per step.  Each page's (layer, head) record arrives
-// in shared memory as two bulk copies (K half, V half) that the warp issues
-// into its own ring (mbarrier completion, bounded waits).
-// Pass A: the int8 dots on tensor cores (mma.sync s8, exact int32), then
-// (dot * ks) * (qs / sqrt(d)) per position into a shared score buffer.
-// Softmax in the reference's order: max, exp(s - max) per position, their
-// total summed in position order by one lane, each divided by it.  Pass B:
-// out[d] += (p * vs) * v[d] in position order, two dims per lane.  Every rounding is the reference's, so the output is
-// the scalar result exactly (the exponential is the correctly rounded one,
-// exp_rn).  The merge of split partials (MergePartials,
-// src/Needle/Blocks.cs:750-817) is not needed: a row is never split.
+// Decode attention, bit for bit the reference's AVX2 attention tier
+// (Attention.GroupAvx2, src/Needle/Blocks.cs:178-541, on an unsplit tile):
+// persistent warps stream (row, head) items from a work list built once per
+// step.  Each page's (layer, head) record arrives in shared memory as two
+// bulk copies (K half, V half) that the warp issues into its own ring
+// (mbarrier completion, bounded waits).  Pass A: the int8 dots on tensor
+// cores (mma.sync s8, exact int32), then (dot * ks) * (qs / sqrt(d)) per
+// position into a shared score buffer.  Softmax in the reference's order:
+// max, e = Ops.Exp(s - max) per position, their total in four partial sums
+// by position modulo 4, inverse = 1 / total.  Pass B: w = e * vs, then
+// acc[d] = fma(w, v[d], acc[d]) in position order, out = acc * inverse.
+// Every rounding is the reference's, so the output is its result exactly.
+// A row is never split, so no merge of partials is needed.
 #include <mutex>
 
 #include "common.cuh"
@@ -239,30 +239,31 @@ __global__ void __launch_bounds__(128) attn_work_kernel(AttnArgs a) {
             a.out[(size_t)row * a.heads * kHeadDim + t] = __int_as_float(0x7fc00000);
 }
 
-// Sum of s[0..n) in position order (one lane: the reference's loop).
-__device__ __forceinline__ float sum_in_order(const float *s, int n) {
+// ExponentiateAcrossPositions' total (src/Needle/Blocks.cs:381-404): four
+// partial sums by position modulo 4 over the whole quads, the positions past
+// the last quad added to the first, combined as (s0 + s1) + (s2 + s3).
+// Lanes 0..3 keep one partial each; every lane returns the total.
+__device__ __forceinline__ float total_four_way(const float *e, int n, int lane) {
+    const int quads = n >> 2;
     float t = 0.0f;
-    int j = 0;
-    for (; j + 4 <= n; j += 4) {
-        const float4 v = *reinterpret_cast<const float4 *>(s + j);
-        t = __fadd_rn(t, v.x);
-        t = __fadd_rn(t, v.y);
-        t = __fadd_rn(t, v.z);
-        t = __fadd_rn(t, v.w);
+    if (lane < 4) {
+#pragma unroll 4
+        for (int i = 0; i < quads; i++) t = __fadd_rn(t, e[4 * i + lane]);
+        if (lane == 0)
+            for (int j = 4 * quads; j < n; j++) t = __fadd_rn(t, e[j]);
     }
-    for (; j < n; j++) t = __fadd_rn(t, s[j]);
-    return t;
+    const float s1 = __shfl_sync(0xffffffffu, t, 1), s2 = __shfl_sync(0xffffffffu, t, 2),
+                s3 = __shfl_sync(0xffffffffu, t, 3);
+    const float total = __fadd_rn(__fadd_rn(t, s1), __fadd_rn(s2, s3));
+    return __shfl_sync(0xffffffffu, total, 0);
 }
 
 // One 16-position chunk of pass B for the lane's two dims: va / vb hold the
 // chunk's V bytes of dim lane and lane + 32, w the chunk's 16 weights.
 // Each int8 becomes an exact float through its biased byte (v ^ 0x80 as the
-// low mantissa byte of 2^23), then acc += w * v per position in order, the
-// product and the sum each rounded.  They are the scalar __fmul_rn /
-// __fadd_rn, which the compiler never merges into a fused multiply-add (the
-// packed-pair forms, even as fma(w, v, -0), were contracted with the sum).
-__device__ __forceinline__ void pv_chunk(float &acc_a, float &acc_b, const uint4 &va, const uint4 &vb,
-                                         const float *w) {
+// low mantissa byte of 2^23), then acc = fma(w, v, acc) per position in
+// order (AccumulateFloat's Fma.MultiplyAdd), both dims in one packed fma.
+__device__ __forceinline__ uint64_t pv_chunk(uint64_t acc, const uint4 &va, const uint4 &vb, const float *w) {
     const uint32_t wa[4] = {va.x ^ 0x80808080u, va.y ^ 0x80808080u, va.z ^ 0x80808080u, va.w ^ 0x80808080u};
     const uint32_t wb[4] = {vb.x ^ 0x80808080u, vb.y ^ 0x80808080u, vb.z ^ 0x80808080u, vb.w ^ 0x80808080u};
     const uint64_t bias = f2_pack(-8388736.0f, -8388736.0f);  // -(2^23 + 128)
@@ -274,12 +275,11 @@ __device__ __forceinline__ void pv_chunk(float &acc_a, float &acc_b, const uint4
         for (int i = 0; i < 4; i++) {
             const float fa = __uint_as_float(__byte_perm(wa[q], 0x4B000000u, 0x7540u + i));
             const float fb = __uint_as_float(__byte_perm(wb[q], 0x4B000000u, 0x7540u + i));
-            float va_f, vb_f;
-            f2_unpack(f2_add(f2_pack(fa, fb), bias), va_f, vb_f);  // exact: both are integers below 2^24
-            acc_a = __fadd_rn(acc_a, __fmul_rn(ww[i], va_f));
-            acc_b = __fadd_rn(acc_b, __fmul_rn(ww[i], vb_f));
+            const uint64_t v = f2_add(f2_pack(fa, fb), bias);  // exact: both are integers below 2^24
+            acc = f2_fma(f2_pack(ww[i], ww[i]), v, acc);
         }
     }
+    return acc;
 }
 
 // One (row, head) item as a warp holds it in registers: its work record
@@ -376,10 +376,11 @@ __device__ __forceinline__ void attn_issue(const AttnArgs &a, uint8_t *wsm, int 
 //    cores (mma.sync m16n8k32 s8, K as A, the query in every B column; lane
 //    (gid, tig) keeps positions 16*tig + gid and + 8), then
 //    s = (dot * ks) * (qs / sqrt(d)) into the warp's score buffer;
-//  * softmax as Scalar.Softmax: max, e = exp_rn(s - max) per position, their
-//    total summed in position order by one lane, p = e / total;
-//  * pass B: weights w = p * vs per position, then out[d] += w * v[d] in
-//    position order, two dims (lane, lane + 32) per lane.
+//  * softmax as the AVX2 tier: max, e = Ops.Exp(s - max) per position,
+//    their total in four partial sums by position modulo 4, 1 / total;
+//  * pass B: weights w = e * vs per position, then acc[d] = fma(w, v[d],
+//    acc[d]) in position order, two dims (lane, lane + 32) per lane;
+//    out = acc * (1 / total).
 // The next item's claim, record and query are loaded into registers while
 // the current one computes, each used only a phase after its load was issued.
 __global__ void __launch_bounds__(kAttnThreads, 3) attn_decode_kernel(AttnArgs a) {
@@ -472,19 +473,16 @@ __global__ void __launch_bounds__(kAttnThreads, 3) attn_decode_kernel(AttnArgs a
         if (timed_out) break;
         // the next item's record (the claim has long returned)
         item_fetch_record(a, __shfl_sync(0xffffffffu, claim, 0), n_work, lane, nx);
-        // ---- softmax (Scalar.Softmax): exp(s - peak), total in position order, p = e / total ----
+        // ---- softmax (Normalizers, ExponentiateAcrossPositions): e = Ops.Exp(s - peak) ----
         peak = warp_max_f(peak);
         __syncwarp();
-        for (int j = lane; j < len; j += 32) sc[j] = exp_rn(__fsub_rn(sc[j], peak));
+        for (int j = lane; j < len; j += 32) sc[j] = exp_simd(__fsub_rn(sc[j], peak));
         __syncwarp();
-        float total = lane == 0 ? sum_in_order(sc, len) : 0.0f;
-        total = __shfl_sync(0xffffffffu, total, 0);
-        for (int j = lane; j < len; j += 32) sc[j] = __fdiv_rn(sc[j], total);
-        __syncwarp();
+        const float inverse = __fdiv_rn(1.0f, total_four_way(sc, len, lane));
         item_fetch_query(a, lane, nx);
         next_ready = true;
-        // ---- pass B: out[d] += (p_j * vs_j) * v_j[d] in position order ----
-        float acc_a = 0.0f, acc_b = 0.0f;  // dims lane, lane + 32
+        // ---- pass B (ValuesFloat, AccumulateFloat): acc[d] = fma(e_j * vs_j, v_j[d], acc[d]) ----
+        uint64_t acc = f2_pack(0.0f, 0.0f);  // dims lane, lane + 32
         for (int pg = 0; pg < n_pages; pg++) {
             const int stage = st.consumed % kAttnStages;
             if (!mbar_wait_bounded(&full[stage], (st.consumed / kAttnStages) & 1, kWaitLimit)) {
@@ -494,7 +492,7 @@ __global__ void __launch_bounds__(kAttnThreads, 3) attn_decode_kernel(AttnArgs a
             const uint8_t *blk = wsm + stage * kKvHalfBytes;  // [V scales][V dim-major]
             const float *vs = reinterpret_cast<const float *>(blk);
             const int valid = min(kPagePositions, len - pg * kPagePositions);
-            // positions past the row's end get weight 0: 0 * v adds a zero, which leaves acc unchanged
+            // positions past the row's end get weight 0: fma(0, v, acc) is acc
             wbuf[lane] = lane < valid ? __fmul_rn(sc[pg * kPagePositions + lane], vs[lane]) : 0.0f;
             wbuf[lane + 32] = lane + 32 < valid ? __fmul_rn(sc[pg * kPagePositions + lane + 32], vs[lane + 32]) : 0.0f;
             uint4 va[4], vb[4];
@@ -509,14 +507,16 @@ __global__ void __launch_bounds__(kAttnThreads, 3) attn_decode_kernel(AttnArgs a
             st.consumed++;
             attn_issue(a, wsm, flags, full, st, cur, nx, next_ready, lane);
 #pragma unroll
-            for (int ch = 0; ch < 4; ch++) pv_chunk(acc_a, acc_b, va[ch], vb[ch], wbuf + 16 * ch);
+            for (int ch = 0; ch < 4; ch++) acc = pv_chunk(acc, va[ch], vb[ch], wbuf + 16 * ch);
             __syncwarp();  // the weights are read before the next page rewrites them
         }
         if (timed_out) break;
         float *out = a.out + ((size_t)cur.row * a.heads + cur.head) * kHeadDim;
+        float acc_a, acc_b;
+        f2_unpack(acc, acc_a, acc_b);
         const float nan = __int_as_float(0x7fc00000);
-        out[lane] = poisoned ? nan : acc_a;
-        out[lane + 32] = poisoned ? nan : acc_b;
+        out[lane] = poisoned ? nan : __fmul_rn(acc_a, inverse);
+        out[lane + 32] = poisoned ? nan : __fmul_rn(acc_b, inverse);
         // the next item becomes current, with the copies already issued for it
         cur = nx;
         st.k_cur = st.k_next;

@@ -121,41 +121,31 @@ __device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
     return r;
 }
 
-// exp of a float, rounded to nearest float: the reference's MathF.Exp,
-// which calls the C runtime's expf (a nearly correctly rounded function).
-// Computed here in double precision from the mathematics, with IEEE
-// operations only, so that the CPU oracle, which restates the same steps,
-// gets the same bits: Cody and Waite's argument reduction
-// x = k*ln2 + r, k = rint(x/ln2), with ln2 split into a high part whose
-// products with k are exact and a low part (the split published with
-// fdlibm), then exp(r) by its Taylor series to degree 13 in Horner form with
-// fused multiply-adds, scaled by 2^k (exact) and rounded once to float.  The
-// relative error before that rounding is below 1e-15, so the result is the
-// correctly rounded float unless exp(x) lies within about 1e-15 of a
-// rounding midpoint.
-__device__ __forceinline__ float exp_rn(float x) {
-    if (x != x) return x;
-    if (x > 89.0f) return __int_as_float(0x7f800000);  // above the float range
-    if (x < -104.0f) return 0.0f;                        // below half the smallest subnormal
-    const double xd = (double)x;
-    const double k = rint(__dmul_rn(xd, 1.4426950408889634));
-    const double r = __dsub_rn(__dsub_rn(xd, __dmul_rn(k, 6.93147180369123816490e-01)),
-                               __dmul_rn(k, 1.90821492927058770002e-10));
-    double p = 1.6059043836821614599e-10;   // 1/13!
-    p = __fma_rn(p, r, 2.0876756987868098979e-09);   // 1/12!
-    p = __fma_rn(p, r, 2.5052108385441718775e-08);   // 1/11!
-    p = __fma_rn(p, r, 2.7557319223985890653e-07);   // 1/10!
-    p = __fma_rn(p, r, 2.7557319223985890653e-06);   // 1/9!
-    p = __fma_rn(p, r, 2.4801587301587301587e-05);   // 1/8!
-    p = __fma_rn(p, r, 1.9841269841269841270e-04);   // 1/7!
-    p = __fma_rn(p, r, 1.3888888888888888889e-03);   // 1/6!
-    p = __fma_rn(p, r, 8.3333333333333333333e-03);   // 1/5!
-    p = __fma_rn(p, r, 4.1666666666666666667e-02);   // 1/4!
-    p = __fma_rn(p, r, 1.6666666666666666667e-01);   // 1/3!
-    p = __fma_rn(p, r, 0.5);
-    p = __fma_rn(p, r, 1.0);
-    p = __fma_rn(p, r, 1.0);
-    return __double2float_rn(scalbn(p, (int)k));
+// Ops.Exp (src/Needle/Ops.cs:16-31), the reference's SIMD exponential, which
+// its AVX2 attention softmax and vector sigmoid use: clamp to [-87.3, 88.7]
+// (a NaN becomes -87.3, as maxps returns its second operand), n = nearest
+// integer of x * log2(e), r = x - n*ln2 in two fused steps, a degree-5
+// polynomial by fused multiply-adds, y = p*r^2 + (r + 1), times 2^n built in
+// the exponent bits.  Each step is one IEEE operation (explicit fma, mul and
+// add intrinsics), so the CPU oracle, which takes the same steps, gets the
+// same bits.
+__device__ __forceinline__ float exp_simd(float x) {
+    x = fminf(fmaxf(x, -87.3f), 88.7f);
+    const float n = rintf(__fmul_rn(x, 1.44269504f));
+    float r = __fmaf_rn(-n, 0.693359375f, x);
+    r = __fmaf_rn(-n, -2.12194440e-4f, r);
+    float p = 1.9875691500e-4f;
+    p = __fmaf_rn(p, r, 1.3981999507e-3f);
+    p = __fmaf_rn(p, r, 8.3334519073e-3f);
+    p = __fmaf_rn(p, r, 4.1665795894e-2f);
+    p = __fmaf_rn(p, r, 1.6666665459e-1f);
+    p = __fmaf_rn(p, r, 5.0000001201e-1f);
+    const float y = __fmaf_rn(p, __fmul_rn(r, r), __fadd_rn(r, 1.0f));
+    return __fmul_rn(y, __int_as_float(((int)n + 127) << 23));
+}
+// Ops.Sigmoid (src/Needle/Ops.cs:36-40): 1 / (1 + Exp(0 - x)).
+__device__ __forceinline__ float sigmoid_simd(float x) {
+    return __fdiv_rn(1.0f, __fadd_rn(1.0f, exp_simd(__fsub_rn(0.0f, x))));
 }
 #endif
 

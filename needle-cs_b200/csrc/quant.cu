@@ -7,7 +7,7 @@
 // RMSNorm sum of squares runs left to right on one lane, as
 // Scalar.SumOfSquares does (src/Needle/Scalar.cs:206-211), from squares the
 // other lanes compute, so the normalised row is the scalar one bit for bit.
-// SiLU's exponential is exp_rn, the correctly rounded one.
+// SiLU's sigmoid is the reference's vector one (Ops.Sigmoid with Ops.Exp).
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -161,7 +161,7 @@ __global__ void __launch_bounds__(kRowThreads) row_quantize_kernel(const float *
                 const float *uu = reinterpret_cast<const float *>(&u);
 #pragma unroll
                 for (int e = 0; e < 4; e++) {
-                    const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, exp_rn(-g[e])));
+                    const float sig = sigmoid_simd(g[e]);
                     g[e] = __fmul_rn(__fmul_rn(g[e], sig), uu[e]);
                 }
             }

@@ -23,7 +23,7 @@ __global__ void bounded_wait_kernel(uint32_t tests, int *status) {
 
 __global__ void exp_kernel(const float *x, int n, float *y) {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i < n) y[i] = exp_rn(x[i]);
+    if (i < n) y[i] = exp_simd(x[i]);
 }
 
 }  // namespace
@@ -51,8 +51,9 @@ NDL_API int ndl_selftest_bounded_wait(int tests) {
     return NDL_OK;
 }
 
-// exp_rn, the library's float exponential (the one its softmax and SiLU
-// use), over n device floats: lets a test pin it to the CPU oracle's.
+// exp_simd, the library's float exponential (Ops.Exp, the one its softmax
+// and SiLU use), over n device floats: lets a test pin it to the CPU
+// oracle's.
 NDL_API int ndl_selftest_exp(const float *x, int n, float *y, void *stream) {
     NDL_REQUIRE(n >= 0 && (n == 0 || (x && y)), "bad arguments");
     if (n == 0) return NDL_OK;

@@ -65,7 +65,7 @@ __global__ void __launch_bounds__(256) swiglu_quantize_kernel(const float *__res
     float peak = 0.0f;
     for (int i = lane; i < ffn; i += 32) {
         const float gv = g[i];
-        const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, exp_rn(-gv)));
+        const float sig = sigmoid_simd(gv);
         const float v = __fmul_rn(__fmul_rn(gv, sig), u[i]);
         a[i] = v;
         peak = fmaxf(peak, fabsf(v));

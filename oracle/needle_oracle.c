@@ -139,6 +139,41 @@ void ndo_exp_rn(const float *x, int n, float *y) {
     for (int i = 0; i < n; i++) y[i] = exp_rn(x[i]);
 }
 
+/* Ops.Exp (src/Needle/Ops.cs:16-31), the reference's SIMD exponential, which
+ * its AVX2 attention softmax (Blocks.cs:362-404) and vector sigmoid
+ * (Ops.cs:36-40) use, restated for one lane: clamp to [-87.3, 88.7] (a NaN
+ * becomes -87.3, as maxps returns its second operand), n = nearest integer of
+ * x * log2(e), r = x - n*ln2 in two fused steps, a degree-5 polynomial by
+ * fused multiply-adds, y = p*r^2 + (r + 1), times 2^n built in the exponent
+ * bits.  Every step is one IEEE operation, so the CUDA kernels, which take the
+ * same steps, return the same bits.  It agrees with expf to within about
+ * 2e-6 relative (tests/Needle.Tests/KernelTests.cs:35-43). */
+static float ops_exp(float x) {
+    x = fminf(fmaxf(x, -87.3f), 88.7f);
+    const float n = rintf(x * 1.44269504f);
+    float r = fmaf(-n, 0.693359375f, x);
+    r = fmaf(-n, -2.12194440e-4f, r);
+    float p = 1.9875691500e-4f;
+    p = fmaf(p, r, 1.3981999507e-3f);
+    p = fmaf(p, r, 8.3334519073e-3f);
+    p = fmaf(p, r, 4.1665795894e-2f);
+    p = fmaf(p, r, 1.6666665459e-1f);
+    p = fmaf(p, r, 5.0000001201e-1f);
+    const float y = fmaf(p, r * r, r + 1.0f);
+    const uint32_t bits = (uint32_t)((int32_t)n + 127) << 23;
+    float scale;
+    memcpy(&scale, &bits, sizeof scale);
+    return y * scale;
+}
+
+/* Ops.Exp over an array (for the tests). */
+void ndo_exp_simd(const float *x, int n, float *y) {
+    for (int i = 0; i < n; i++) y[i] = ops_exp(x[i]);
+}
+
+/* Ops.Sigmoid (src/Needle/Ops.cs:36-40): 1 / (1 + Exp(0 - x)). */
+static float ops_sigmoid(float x) { return 1.0f / (1.0f + ops_exp(0.0f - x)); }
+
 static float maxf_cs(float a, float b) { return a > b ? a : (b > a ? b : (a == a ? a : b)); }
 
 /* Scalar.AbsMax (Scalar.cs:55-60). */
@@ -287,10 +322,10 @@ void ndo_zero_centered_rms(const float *x, const float *scale, int n, float *dst
     for (int i = 0; i < n; i++) dst[i] = ((1.0f + scale[i]) * x[i]) * inv;
 }
 
-/* SwiGLU from Scalar.Silu and Scalar.Glu (Scalar.cs:196-199,280-283):
- * dst = (g*sigmoid(g))*u. */
+/* SwiGLU from the reference's AVX2 Silu / Glu (src/Needle/Ops.cs:90-105,
+ * 1013-1024: x * Sigmoid(x) on vectors): dst = (g * Ops.Sigmoid(g)) * u. */
 void ndo_swiglu(const float *gate, const float *up, int n, float *dst) {
-    for (int i = 0; i < n; i++) dst[i] = (gate[i] * ndo_sigmoid(gate[i])) * up[i];
+    for (int i = 0; i < n; i++) dst[i] = (gate[i] * ops_sigmoid(gate[i])) * up[i];
 }
 
 /* ------------------------------------------------------------------------ */
@@ -770,6 +805,49 @@ void ndo_attention_head(const int8_t *query, float query_scale, const int8_t *ke
     }
 }
 
+/* Attention.GroupAvx2 (src/Needle/Blocks.cs:178-185) for one head of an
+ * unsplit tile, the reference's AVX2 attention tier: ScoresAvx2 (:274-336,
+ * exact int32 dots, s = (dot * ks) * (qs / sqrt(d))), Normalizers (:188-199)
+ * with ExponentiateAcrossPositions (:362-404: e = Ops.Exp(s - max), summed in
+ * four partial sums by position modulo 4 with the tail positions in the
+ * first, combined as (s0 + s1) + (s2 + s3); inverse = 1 / total), ValuesFloat
+ * (:413-420: w = e * vs) and AccumulateFloat (:494-541: acc = fma(w, v, acc)
+ * in position order; out = acc * inverse). */
+void ndo_attention_head_simd(const int8_t *query, float query_scale, const int8_t *keys, const float *key_scales,
+                             const int8_t *values, const float *value_scales, int key_stride, int value_stride,
+                             int scale_stride, int first, int last, int qk_dim, int v_dim, float inv_sqrt_dim,
+                             float *scores, float *output) {
+    int count = last - first + 1;
+    float scale = query_scale * inv_sqrt_dim;
+    float peak = -INFINITY;
+    for (int s = 0; s < count; s++) {
+        const int8_t *key = keys + (size_t)(first + s) * key_stride;
+        int dot = 0;
+        for (int d = 0; d < qk_dim; d++) dot += query[d] * key[d];
+        scores[s] = ((float)dot * key_scales[(size_t)(first + s) * scale_stride]) * scale;
+        peak = maxf_cs(peak, scores[s]);
+    }
+    float sum[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    int s = 0;
+    for (; s + 4 <= count; s += 4)
+        for (int k = 0; k < 4; k++) {
+            scores[s + k] = ops_exp(scores[s + k] - peak);
+            sum[k] += scores[s + k];
+        }
+    for (; s < count; s++) {
+        scores[s] = ops_exp(scores[s] - peak);
+        sum[0] += scores[s];
+    }
+    const float inverse = 1.0f / ((sum[0] + sum[1]) + (sum[2] + sum[3]));
+    for (s = 0; s < count; s++) scores[s] *= value_scales[(size_t)(first + s) * scale_stride];
+    for (int d = 0; d < v_dim; d++) output[d] = 0.0f;
+    for (s = 0; s < count; s++) {
+        const int8_t *row = values + (size_t)(first + s) * value_stride;
+        for (int d = 0; d < v_dim; d++) output[d] = fmaf(scores[s], (float)row[d], output[d]);
+    }
+    for (int d = 0; d < v_dim; d++) output[d] *= inverse;
+}
+
 /* Attention.MergePartials, non-SIMD branch (src/Needle/Blocks.cs:750-817). */
 void ndo_merge_partials(const float *partials, int count, int heads, int stride, int peak_off, float *output) {
     float weights[64];
@@ -989,8 +1067,8 @@ int ndo_decoder_row_cross(const ndo_decoder *m, int token, int pos, int capacity
             lvs[(size_t)pos * H + hh] = ndo_quantize_int8(v + hh * hd, hd, lv + (size_t)pos * width + hh * hd);
         }
         for (int hh = 0; hh < H; hh++)
-            ndo_attention_head(qq + hh * hd, qs[hh], lk + hh * hd, lks + hh, lv + hh * hd, lvs + hh, width, width, H, 0,
-                               pos, hd, hd, inv_sqrt, scores, o + hh * hd, NULL);
+            ndo_attention_head_simd(qq + hh * hd, qs[hh], lk + hh * hd, lks + hh, lv + hh * hd, lvs + hh, width, width,
+                                    H, 0, pos, hd, hd, inv_sqrt, scores, o + hh * hd);
         sa = ndo_quantize_int8(o, d, qa);
         ndo_matmul_i8g32(m->w_o[l], m->s_o[l], d, d, qa, &sa, 1, NULL, proj, d);
         for (int i = 0; i < d; i++) x[i] = x[i] + proj[i];
@@ -1003,8 +1081,8 @@ int ndo_decoder_row_cross(const ndo_decoder *m, int token, int pos, int capacity
             const int8_t *mk = mem_k + (size_t)l * frames * width, *mv = mem_v + (size_t)l * frames * width;
             const float *mks = mem_ks + (size_t)l * frames * H, *mvs = mem_vs + (size_t)l * frames * H;
             for (int hh = 0; hh < H; hh++)
-                ndo_attention_head(qq + hh * hd, qs[hh], mk + hh * hd, mks + hh, mv + hh * hd, mvs + hh, width, width,
-                                   H, 0, frames - 1, hd, hd, inv_sqrt, scores, o + hh * hd, NULL);
+                ndo_attention_head_simd(qq + hh * hd, qs[hh], mk + hh * hd, mks + hh, mv + hh * hd, mvs + hh, width,
+                                        width, H, 0, frames - 1, hd, hd, inv_sqrt, scores, o + hh * hd);
             sa = ndo_quantize_int8(o, d, qa);
             ndo_matmul_i8g32(m->w_co[l], m->s_co[l], d, d, qa, &sa, 1, NULL, proj, d);
             for (int i = 0; i < d; i++) x[i] = x[i] + proj[i];

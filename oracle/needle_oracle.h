@@ -13,7 +13,10 @@
  * summation, MathF.Cos/Sin/Pow mapped to the C library's cosf/sinf/powf
  * (which is what .NET calls on Linux), and MathF.Exp to exp_rn, the float
  * exponential rounded to nearest, computed from the mathematics with IEEE
- * double operations (needle_oracle.c).
+ * double operations (needle_oracle.c).  The decoder's attention and SiLU
+ * restate the reference's AVX2 tier instead (Attention.GroupAvx2 and the
+ * vector Silu/Glu, with Ops.Exp): fused multiply-adds where it uses them,
+ * its partial sums in its order.
  */
 #ifndef NEEDLE_ORACLE_H
 #define NEEDLE_ORACLE_H
@@ -37,6 +40,7 @@ uint16_t ndo_half_bits(float value);
 
 /* ---- the exponential (MathF.Exp) over an array ---- */
 void ndo_exp_rn(const float *x, int n, float *y);
+void ndo_exp_simd(const float *x, int n, float *y);
 
 /* ---- row primitives (src/Needle/Scalar.cs) ---- */
 float ndo_abs_max(const float *x, int n);
@@ -117,6 +121,10 @@ void ndo_attention_head(const int8_t *query, float query_scale, const int8_t *ke
                         const int8_t *values, const float *value_scales, int key_stride, int value_stride,
                         int scale_stride, int first, int last, int qk_dim, int v_dim, float inv_sqrt_dim,
                         float *scores, float *output, float *probabilities);
+void ndo_attention_head_simd(const int8_t *query, float query_scale, const int8_t *keys, const float *key_scales,
+                             const int8_t *values, const float *value_scales, int key_stride, int value_stride,
+                             int scale_stride, int first, int last, int qk_dim, int v_dim, float inv_sqrt_dim,
+                             float *scores, float *output);
 /* Attention.MergePartials scalar branch (src/Needle/Blocks.cs:750-817):
  * partial c = {out[heads*64] at c*stride, peak[h] at c*stride+peak_off,
  * sum[h] at c*stride+peak_off+8}. */

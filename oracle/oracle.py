@@ -33,6 +33,7 @@ _SIGS = {
     "ndo_fake_a8": (F, [P, I]),
     "ndo_half_to_single": (F, [_c.c_uint16]),
     "ndo_exp_rn": (None, [P, I, P]),
+    "ndo_exp_simd": (None, [P, I, P]),
     "ndo_hadamard128": (None, [P, P]),
     "ndo_planes": (None, [P, I, P, _c.POINTER(I)]),
     "ndo_sigmoid": (F, [F]),
@@ -65,6 +66,7 @@ _SIGS = {
     "ndo_conf_logit": (F, [P, P, I, I, P, P, P, F, P, I, P]),
     "ndo_matmul_i8g32": (None, [P, P, I, I, P, P, I, P, P, I]),
     "ndo_attention_head": (None, [P, F, P, P, P, P, I, I, I, I, I, I, I, F, P, P, P]),
+    "ndo_attention_head_simd": (None, [P, F, P, P, P, P, I, I, I, I, I, I, I, F, P, P]),
     "ndo_merge_partials": (None, [P, I, I, I, I, P]),
     "ndo_argmax": (I, [P, I]),
     "ndo_argmax_masked": (I, [P, P, I, I]),
@@ -143,6 +145,14 @@ def exp_rn(x):
     x = f32(x)
     y = np.empty_like(x)
     lib().ndo_exp_rn(ptr(x), x.size, ptr(y))
+    return y
+
+
+def exp_simd(x):
+    """Ops.Exp, the reference's SIMD exponential, as the oracle restates it."""
+    x = f32(x)
+    y = np.empty_like(x)
+    lib().ndo_exp_simd(ptr(x), x.size, ptr(y))
     return y
 
 
@@ -313,6 +323,18 @@ def attention_head(query, query_scale, keys, key_scales, values, value_scales, k
     lib().ndo_attention_head(ptr(query), query_scale, ptr(keys), ptr(key_scales), ptr(values), ptr(value_scales),
                              key_stride, value_stride, scale_stride, first, last, qk_dim, v_dim, inv_sqrt_dim,
                              ptr(scores), ptr(out), ptr(probabilities))
+    return out
+
+
+def attention_head_simd(query, query_scale, keys, key_scales, values, value_scales, key_stride, value_stride,
+                        scale_stride, first, last, qk_dim, v_dim, inv_sqrt_dim):
+    """Attention.GroupAvx2 on one head of an unsplit tile (the AVX2 tier)."""
+    count = last - first + 1
+    scores = np.empty(max(count, 1) + 8, np.float32)
+    out = np.empty(v_dim, np.float32)
+    lib().ndo_attention_head_simd(ptr(query), query_scale, ptr(keys), ptr(key_scales), ptr(values),
+                                  ptr(value_scales), key_stride, value_stride, scale_stride, first, last, qk_dim,
+                                  v_dim, inv_sqrt_dim, ptr(scores), ptr(out))
     return out
 
 

@@ -78,15 +78,19 @@ def make_case(seed, lengths, heads, layers=2, layer=1, max_pages=17):
                 row_pos=np.array([n - 1 for n in lengths], np.int32), heads=heads, layer=layer)
 
 
-def oracle_out(oracle, case, lengths):
+def oracle_out(oracle, case, lengths, tier="simd"):
+    """The oracle's attention of every (row, head): the reference's AVX2 tier
+    (Attention.GroupAvx2, which the CUDA kernel follows bit for bit) or its
+    scalar tier (Scalar.AttentionHead)."""
     rows, heads = len(lengths), case["heads"]
     out = np.zeros((rows, heads, 64), np.float32)
     for r, n in enumerate(lengths):
         for h in range(heads):
             keys = np.ascontiguousarray(case["K"][r, :n, h])
             vals = np.ascontiguousarray(case["V"][r, :n, h])
-            out[r, h] = oracle.attention_head(case["Q"][r, h], np.float32(case["QS"][r, h]), keys,
-                                              np.ascontiguousarray(case["KS"][r, :n, h]), vals,
-                                              np.ascontiguousarray(case["VS"][r, :n, h]), 64, 64, 1, 0, n - 1, 64,
-                                              64, np.float32(0.125))
+            fn = oracle.attention_head_simd if tier == "simd" else oracle.attention_head
+            out[r, h] = fn(case["Q"][r, h], np.float32(case["QS"][r, h]), keys,
+                           np.ascontiguousarray(case["KS"][r, :n, h]), vals,
+                           np.ascontiguousarray(case["VS"][r, :n, h]), 64, 64, 1, 0, n - 1, 64, 64,
+                           np.float32(0.125))
     return out

@@ -1,10 +1,11 @@
 """Standalone paged decode attention (ndl_attention_paged) against the
-oracle's Scalar.AttentionHead restatement: bit-identical.  The kernel keeps
-the reference's order of every rounding (scores, max, exponentials, the
-total summed in position order, p = e / total, out += (p * vs) * v in
-position order), so no tolerance is needed; the reference's own
-AttentionTile conformance bar would be 3e-5 x peak |output|
-(tests/Needle.Tests/KernelTests.cs:231-236)."""
+oracle: bit-identical to its restatement of the reference's AVX2 attention
+tier (Attention.GroupAvx2: scores, max, Ops.Exp, the four-way partial sums,
+1 / total, fma accumulation of e * vs * v in position order, the final
+scale).  The oracle keeps that tier within the reference's own tier-to-tier
+bar of Scalar.AttentionHead, 3e-5 x peak |output|
+(tests/Needle.Tests/KernelTests.cs:231-236; tests/test_exp_oracle.py).
+"""
 import numpy as np
 import pytest
 import torch

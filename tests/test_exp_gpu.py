@@ -1,5 +1,5 @@
-"""The library's float exponential (exp_rn, used by the attention softmax
-and the SiLU gate) against the oracle's restatement of MathF.Exp."""
+"""The library's float exponential (Ops.Exp, used by the attention softmax
+and the SiLU gate) against the oracle's restatement of it."""
 import numpy as np
 import pytest
 
@@ -8,9 +8,9 @@ pytestmark = pytest.mark.gpu
 
 def test_device_exp_equals_oracle_exp(pkg, oracle, cuda):
     """The exponential of the attention softmax and the SiLU gate: the
-    device's exp_rn returns the oracle's bits on every input (same
-    double-precision steps on both sides), which keeps decoder logits
-    bit-comparable through 12 layers."""
+    device's Ops.Exp returns the oracle's bits on every input (the same IEEE
+    steps on both sides), which keeps decoder logits bit-comparable through
+    12 layers."""
     import torch
 
     from needle_cs_b200._native import call
@@ -24,6 +24,6 @@ def test_device_exp_equals_oracle_exp(pkg, oracle, cuda):
     call("ndl_selftest_exp", xd.data_ptr(), x.size, yd.data_ptr(), torch.cuda.current_stream().cuda_stream)
     torch.cuda.synchronize()
     got = yd.cpu().numpy()
-    ref = oracle.exp_rn(x)
+    ref = oracle.exp_simd(x)
     same = (got.view(np.int32) == ref.view(np.int32)) | (np.isnan(got) & np.isnan(ref))
     assert same.all(), (x[~same][:5], got[~same][:5], ref[~same][:5])
