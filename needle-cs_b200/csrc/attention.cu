@@ -182,7 +182,10 @@ int launch_cross_kv_write(const float *y, int frames, int heads, const int32_t *
 
 // ------------------------------------------------------ decode attention --
 constexpr int kAttnWarps = 4;   // warps per CTA; each works its own items
-constexpr int kAttnStages = 3;  // ring stages (half records) per warp
+#ifndef NDL_ATTN_STAGES
+#define NDL_ATTN_STAGES 3
+#endif
+constexpr int kAttnStages = NDL_ATTN_STAGES;  // ring stages (half records) per warp
 constexpr int kAttnThreads = 32 * kAttnWarps;
 constexpr int kAttnPageRegs = kAttnMaxPositions / kPagePositions / 32;  // page ids per lane of an item
 constexpr uint32_t kWaitLimit = 1u << 22;
@@ -408,7 +411,7 @@ __global__ void __launch_bounds__(kAttnThreads, 3) attn_decode_kernel(AttnArgs a
     AttnStream st{0u, 0u, 0, 0};
     AttnItemRegs cur, nx;
     item_fetch_record(a, blockIdx.x * kAttnWarps + warp, n_work, lane, cur);
-    item_fetch_query(a, lane, cur);
+    bool query_ready = false;  // cur's query scale and bytes are in registers
     nx.item = n_work;
     nx.pages = 0;
     bool timed_out = false;
@@ -417,7 +420,7 @@ __global__ void __launch_bounds__(kAttnThreads, 3) attn_decode_kernel(AttnArgs a
             int claim = 0;
             if (lane == 0) claim = W + atomicAdd(next_item, 1);
             item_fetch_record(a, __shfl_sync(0xffffffffu, claim, 0), n_work, lane, cur);
-            item_fetch_query(a, lane, cur);
+            query_ready = false;
             st.k_cur = 0;
             continue;
         }
@@ -425,6 +428,7 @@ __global__ void __launch_bounds__(kAttnThreads, 3) attn_decode_kernel(AttnArgs a
         if (lane == 0) claim = W + atomicAdd(next_item, 1);  // the next item, read after pass A
         bool next_ready = false;
         attn_issue(a, wsm, flags, full, st, cur, nx, next_ready, lane);
+        if (!query_ready) item_fetch_query(a, lane, cur);  // lands while the first copies are in flight
         const float scale = __fmul_rn(cur.qs, a.inv_sqrt_d);
         const uint4 qv = cur.q;
         const int len = cur.len, n_pages = cur.pages;
@@ -519,6 +523,7 @@ __global__ void __launch_bounds__(kAttnThreads, 3) attn_decode_kernel(AttnArgs a
         out[lane + 32] = poisoned ? nan : __fmul_rn(acc_b, inverse);
         // the next item becomes current, with the copies already issued for it
         cur = nx;
+        query_ready = true;
         st.k_cur = st.k_next;
         st.k_next = 0;
         nx.item = n_work;

@@ -97,3 +97,26 @@ def oracle_greedy(ops, oracle, dec, seed, session, length, token, steps):
         ids.append(token)
         pos += 1
     return ids, logits
+
+
+def oracle_request(oracle, dec, prompt, max_new, mask, vocab, stop=-1):
+    """One request on the oracle, as a session serves it alone: the prompt
+    one row at a time from an empty cache, then greedy decoding with the
+    request's vocabulary mask (Ops.ArgMaxMasked; plain argmax without a
+    mask) until max_new tokens, the stop token or an empty mask."""
+    kv = dec.new_kv()
+    pos = 0
+    for t in prompt:
+        logits = dec.row(int(t), pos, kv)
+        pos += 1
+    out = []
+    while True:
+        tok = oracle.argmax_masked(logits, mask, vocab) if mask is not None else int(np.argmax(logits))
+        if tok < 0:
+            break
+        out.append(int(tok))
+        if len(out) >= max_new or tok == stop:
+            break
+        logits = dec.row(int(tok), pos, kv)
+        pos += 1
+    return out

@@ -86,3 +86,29 @@ def test_beam_search_matches_oracle(whistle, oracle):
         ref, ref_score = oracle.beam_search(dec, mem, PROMPT, width, steps, eos=50257)
         assert got[i] == ref, (i, got[i], ref)
         assert abs(float(scores[i]) - ref_score) <= 1e-4 * max(1.0, abs(ref_score))
+
+
+def test_beam_search_full_cfg4_matches_oracle(pkg, oracle, cuda):
+    """cfg4's full shape: 1500-frame memories, width 3, up to 128 tokens, on
+    4 utterances at once; every utterance's token sequence equals the
+    oracle's Whistle.BeamSearch restatement and its score is within 1e-4."""
+    from needle_cs_b200.beam import beam_search
+    from needle_cs_b200.engine import BatchedEngine, whistle_decoder
+
+    from decoder_support import parallel_map
+
+    width, steps, frames = 3, 128, 1500
+    utts = [(u, frames, 40 + u) for u in range(4)]
+    with BatchedEngine(whistle_decoder(seed=3), slots=4 + 4 * 2 * width, context_length=1536, chunk_size=16,
+                       max_heads=16) as eng:
+        for slot, n, utt in utts:
+            _memory(eng, slot, n, utt)
+        beam_slots = np.arange(4, 4 + 4 * 2 * width).reshape(4, 2 * width)
+        got, scores = beam_search(eng, [u[0] for u in utts], beam_slots, PROMPT, width=width, max_steps=steps)
+        dec = oracle_decoder(oracle, eng)
+        mems = [_oracle_memory(oracle, dec, eng, n, utt) for _, n, utt in utts]
+
+    refs = parallel_map(lambda i: oracle.beam_search(dec, mems[i], PROMPT, width, steps, eos=50257), range(4))
+    for i, (ref, ref_score) in enumerate(refs):
+        assert got[i] == ref, (i, len(got[i]), len(ref))
+        assert abs(float(scores[i]) - ref_score) <= 1e-4 * max(1.0, abs(ref_score))
