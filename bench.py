@@ -34,6 +34,27 @@ FALLBACK_HBM_GBS = 6650.0
 ATTN_TRAFFIC_PER_ALG_BYTE = 1.076
 
 
+def host_cpu():
+    """The host's CPU model and core count, for the CPU baselines' records."""
+    model = "unknown CPU"
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    model = line.split(":", 1)[1].strip()
+                    break
+    except OSError:
+        pass
+    return model, os.cpu_count() or 1
+
+
+def baseline_label(oracle, threads):
+    model, nproc = host_cpu()
+    env = os.environ.get("NEEDLE_THREADS")
+    return (f"AVX2 restatement of the reference's kernels (oracle/avx2_decoder.c), {threads} threads "
+            f"(NEEDLE_THREADS={env if env else 'unset: all cores'}; nproc {nproc}; {model})")
+
+
 def hbm_peak():
     try:
         with open(PEAKS_PATH) as f:
@@ -150,6 +171,125 @@ def max_over_ranks(value, world):
     return float(t.item())
 
 
+def gather_ranks(values, world):
+    """Every rank's list of floats (rank order), for per-rank reporting."""
+    if world == 1:
+        return [list(values)]
+    import torch
+    import torch.distributed as dist
+
+    device = "cuda" if dist.get_backend() == "nccl" else "cpu"
+    t = torch.tensor(values, dtype=torch.float64, device=device)
+    out = [torch.zeros_like(t) for _ in range(world)]
+    dist.all_gather(out, t)
+    return [[float(v) for v in o.cpu()] for o in out]
+
+
+# ------------------------------------------------- int8 linear records --
+NOMINAL_INT8_TOPS = 4500.0  # B200 dense int8, nominal
+
+
+def int8_peak_tops(device):
+    """A measured int8 tensor-core peak: cuBLASLt's int8 GEMM (torch._int_mm)
+    at 8192^3, best of 5 (the int8 counterpart of the driver's bf16 GEMM
+    peak); the nominal 4.5 POPS when it cannot run."""
+    import torch
+
+    try:
+        a = torch.randint(-127, 128, (8192, 8192), dtype=torch.int8, device=device)
+        b = torch.randint(-127, 128, (8192, 8192), dtype=torch.int8, device=device).t()
+        for _ in range(2):
+            torch._int_mm(a, b)
+        torch.cuda.synchronize()
+        best = None
+        for _ in range(5):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            torch._int_mm(a, b)
+            e1.record()
+            e1.synchronize()
+            ms = e0.elapsed_time(e1)
+            best = ms if best is None else min(best, ms)
+        del a, b
+        return 2 * 8192 ** 3 / (best * 1e-3) / 1e12, "measured: cuBLASLt int8 GEMM (torch._int_mm) 8192^3, best of 5"
+    except Exception as exc:  # an unsupported op on this build: state the nominal figure
+        return NOMINAL_INT8_TOPS, f"nominal dense int8 (torch._int_mm unavailable: {type(exc).__name__})"
+
+
+def linear_records(device):
+    """BASELINE's second and third metrics beside the decode line: the cfg1
+    int8 linear as a GEMV (M = 1 and 16; GB/s of algorithmic bytes, kernel
+    alone over 192 weight copies and per public-API call, as fractions of the
+    measured HBM copy peak; target 0.6) and the tcgen05 GEMM at the cfg5
+    batch shapes (M = 512) and a cfg3 prefill chunk (M = 256) in int8 TOPS as
+    fractions of a measured int8 peak (target 0.5)."""
+    import torch
+
+    ops = __import__("needle_cs_b200.ops", fromlist=["ops"])
+    peak_gbs, _ = hbm_peak()
+    gemv = {}
+    for m in (1, 16):
+        wl = GemvWorkload(m=m)
+        wl.setup(device)
+        for _ in range(3):
+            wl.step()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(10):
+            wl.step()
+        e1.record()
+        e1.synchronize()
+        kernel_gbs = 10 * wl.bytes_per_step() / (e0.elapsed_time(e1) * 1e-3) / 1e9
+        # one public-API call per weight copy (device buffers), back to back
+        y = torch.empty((m, wl.n), dtype=torch.float32, device=device)
+        e0.record()
+        for c in range(wl.copies):
+            ops.matmul_i8g32(wl.q, wl.sa, wl.w[c], wl.sw[c], y=y)
+        e1.record()
+        e1.synchronize()
+        call_gbs = wl.copies * wl.unit_bytes / (e0.elapsed_time(e1) * 1e-3) / 1e9
+        gemv[f"m{m}"] = {"kernel_gbs": round(kernel_gbs, 1), "per_call_gbs": round(call_gbs, 1),
+                         "frac": round(kernel_gbs / peak_gbs, 3), "per_call_frac": round(call_gbs / peak_gbs, 3),
+                         "bytes_per_call": wl.unit_bytes}
+        del wl
+    gemv.update({"peak_gbs": peak_gbs, "target_frac": 0.6,
+                 "shape": "x [M,512] int8 . W [2048,512]^T int8, fp16 scale per 32 columns, 192 weight copies"})
+    peak_tops, peak_src = int8_peak_tops(device)
+    shapes = {"cfg5_qkv": (512, 1536, 512), "cfg5_o": (512, 512, 512), "cfg5_gateup": (512, 4096, 512),
+              "cfg5_down": (512, 512, 2048), "cfg5_head": (512, 8192, 512), "cfg3_chunk_gateup": (256, 4096, 512),
+              "cfg3_chunk_qkv": (256, 1536, 512)}
+    gemm, layer_flops, layer_ms = {}, 0.0, 0.0
+    for name, (m, n, k) in shapes.items():
+        q = torch.randint(-127, 128, (m, k), dtype=torch.int8, device=device)
+        sa = torch.rand(m, device=device) * 0.01
+        w = torch.randint(-127, 128, (n, k), dtype=torch.int8, device=device)
+        sw = torch.full((n, k // 32), 0x2000, dtype=torch.int16, device=device)
+        y = torch.empty((m, n), device=device)
+        for _ in range(3):
+            ops.matmul_i8g32(q, sa, w, sw, y=y)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(20):
+            ops.matmul_i8g32(q, sa, w, sw, y=y)
+        e1.record()
+        e1.synchronize()
+        ms = e0.elapsed_time(e1) / 20
+        tops = 2 * m * n * k / (ms * 1e-3) / 1e12
+        gemm[name] = {"m": m, "n": n, "k": k, "us": round(ms * 1e3, 2), "tops": round(tops, 1),
+                      "frac": round(tops / peak_tops, 4)}
+        if name.startswith("cfg5") and name != "cfg5_head":
+            layer_flops += 2 * m * n * k
+            layer_ms += ms
+    gemm["cfg5_layer"] = {"tops": round(layer_flops / (layer_ms * 1e-3) / 1e12, 1),
+                          "frac": round(layer_flops / (layer_ms * 1e-3) / 1e12 / peak_tops, 4)}
+    gemm.update({"peak_tops": round(peak_tops, 1), "peak_source": peak_src, "target_frac": 0.5,
+                 "kernel": "gemm_i8g32_tc_kernel (tcgen05.mma kind::i8, TMA), 20 back-to-back calls per shape",
+                 "note": "bit-exactness fixes one dequantising fma per (row, column, 32-group) in ascending "
+                         "group order on the CUDA cores"})
+    return gemv, gemm
+
+
 # ------------------------------------------------------------ workloads --
 class GemvWorkload:
     """Config 1: the int8 linear [M,512] x [2048,512]^T with per-32-group fp16
@@ -206,22 +346,34 @@ class GemvWorkload:
         return {"workload": self.name, "m": self.m, "n": self.n, "k": self.k, "weight_copies": self.copies,
                 "group": 32, "l2": "inputs exceed L2 (weights cycled over %d MiB)" % (self.copies * self.n * self.k >> 20)}
 
-    # CPU baseline on a bounded sample: the oracle (scalar restatement).
-    def cpu_sample(self, oracle, budget_s=10.0):
-        ops = self.ops
+    # CPU baseline on a bounded sample: the AVX2 restatement of the reference's
+    # linear on all host cores, weights cycled over copies larger than the LLC
+    # (the reference's kernel bench cycles weight buffers the same way).
+    def cpu_sample(self, oracle, budget_s=10.0, copies=64, reps=5):
         m, n, k = self.m, self.n, self.k
-        x = ops.synth_normal_f32(0, 1, m * k).reshape(m, k)
-        w = ops.synth_int8(0, 2, n * k).reshape(n, k)
-        sw = ops.synth_uniform_f16(0, 3, n * (k // 32), 0.001, 0.02).reshape(n, k // 32)
+        threads = oracle.host_threads()
+        x = oracle.synth_normal(0, 1, m * k).reshape(m, k)
         q, sa = oracle.quantize_rows(x)
-        calls, t0 = 0, time.perf_counter()
-        while True:
-            oracle.matmul_i8g32(q, sa, w, sw)
-            calls += 1
-            dt = time.perf_counter() - t0
-            if dt >= budget_s or calls >= 200:
-                break
-        return calls * self.unit_bytes / dt / 1e9, f"{calls} calls of the M={m} linear, 1 weight set (L2/LLC-warm)"
+        lins = []
+        for c in range(copies):
+            w = oracle.synth_int8(0, 2, n * k, first=c * n * k).reshape(n, k)
+            sw = oracle.synth_uniform_f16(0, 3, n * (k // 32), 0.001, 0.02, first=c * n * (k // 32))
+            lins.append(oracle.AVX2Linear(w, sw.reshape(n, k // 32)))
+        y = np.empty((m, n), np.float32)
+        for lin in lins[:4]:
+            lin.run(q, sa, y, threads)
+        rates, t_end = [], time.perf_counter() + budget_s
+        while len(rates) < reps or (time.perf_counter() < t_end and len(rates) < 50):
+            t0 = time.perf_counter()
+            for lin in lins:
+                lin.run(q, sa, y, threads)
+            rates.append(copies * self.unit_bytes / (time.perf_counter() - t0) / 1e9)
+        for lin in lins:
+            lin.close()
+        med = statistics.median(rates)
+        return med, threads, (f"{len(rates)} reps of the M={m} linear over {copies} weight copies "
+                              f"({copies * n * k >> 20} MiB, beyond the LLC); median {med:.2f}, best "
+                              f"{max(rates):.2f} GB/s; " + baseline_label(oracle, threads))
 
 
 class CqWorkload:
@@ -307,7 +459,8 @@ class CqWorkload:
             dt = time.perf_counter() - t0
             if dt >= budget_s or calls >= 200:
                 break
-        return calls * self.unit_bytes / dt / 1e9, f"{calls} calls of the M={m} CQ matmul, 1 matrix (L2/LLC-warm)"
+        return calls * self.unit_bytes / dt / 1e9, 1, (f"{calls} calls of the M={m} CQ matmul, 1 matrix "
+                                                        f"(L2/LLC-warm), 1 thread of the scalar restatement")
 
 
 class DecodeWorkload:
@@ -432,38 +585,47 @@ class DecodeWorkload:
                 "kv_cache": "paged int8, 64 positions per page, fp32 scale per (position, head)",
                 "greedy": True, "l2": "inputs exceed L2 (paged KV of every session is read each step)"}
 
-    # --- CPU restatement on a bounded sample ---
-    def cpu_sample(self, oracle, budget_s=20.0, threads=None):
-        from concurrent.futures import ThreadPoolExecutor
-
-        syn = __import__("needle_cs_b200.synthetic", fromlist=["synthetic"])
-        _, model = self.model()
-        threads = threads or os.cpu_count() or 1
+    # --- CPU baseline: the AVX2 restatement on all host cores ---
+    def cpu_setup(self, oracle, rows=64, steps=8):
+        """The first `rows` sessions of this GPU's layout (64 = the
+        reference's ForwardBatch row cap, src/Needle/Engine.cs:2306) on the
+        CPU: the decoder's tensors and the sessions' prefix K/V built by the
+        oracle's own generator (nothing from the CUDA library)."""
         gids, lengths, tokens = self.global_layout(0, 1)
-        layers, fnorm, emb, wh, sh = syn.decoder_weights(model)
-        cap = int(lengths.max()) + 2
-        dec = oracle.Decoder(model, layers, fnorm, emb, wh, sh, cap)
-        n = max(1, min(2 * threads, 32))
+        rows = min(rows, len(gids))
+        cap = ((int(lengths[:rows].max()) + steps + 64) // 64) * 64
+        dec = oracle.synthetic_decoder(oracle.DecoderConfig(seed=1), cap)
         kvs = []
-        for j in range(n):
+        for j in range(rows):
             kv = dec.new_kv()
-            for layer in range(model.layers):
-                for kind, (vals, scales) in enumerate((("k", "ks"), ("v", "vs"))):
-                    x = syn.prefix_kv_values(self.seed, int(gids[j]), layer, kind, int(lengths[j]), model.heads)
-                    q, s = oracle.quantize_rows(x.reshape(-1, 64))
-                    kv[vals][layer, :lengths[j]] = q.reshape(int(lengths[j]), -1)
-                    kv[scales][layer, :lengths[j]] = s.reshape(int(lengths[j]), -1)
+            oracle.synthetic_prefix_kv(dec, kv, int(lengths[j]), self.seed, int(gids[j]))
             kvs.append(kv)
+        return dec, kvs, lengths[:rows].astype(np.int32).copy(), tokens[:rows].astype(np.int32).copy()
 
-        def one(j):
-            return dec.row(int(tokens[j]), int(lengths[j]), kvs[j])
+    def cpu_steps(self, oracle, steps, warmup=1, rows=64):
+        """Batched decode steps of `rows` sessions (greedy ids fed back):
+        (tokens/s of each timed step, threads, rows)."""
+        dec, kvs, pos, toks = self.cpu_setup(oracle, rows, steps + warmup)
+        avx = oracle.AVX2Decoder(dec)
+        threads = oracle.host_threads()
+        rates = []
+        for i in range(warmup + steps):
+            t0 = time.perf_counter()
+            logits = avx.step(toks, pos, kvs, threads)
+            dt = time.perf_counter() - t0
+            if i >= warmup:
+                rates.append(len(toks) / dt)
+            toks = logits.argmax(axis=1).astype(np.int32)
+            pos += 1
+        avx.close()
+        return rates, threads, len(toks)
 
-        t0 = time.perf_counter()
-        with ThreadPoolExecutor(max_workers=threads) as pool:
-            list(pool.map(one, range(n)))
-        dt = time.perf_counter() - t0
-        return n / dt, threads, (f"{n} sessions x 1 decode token each (KV lengths {int(lengths[:n].min())}.."
-                                 f"{int(lengths[:n].max())}), {threads} threads of the scalar C restatement")
+    def cpu_sample(self, oracle, reps=5):
+        rates, threads, rows = self.cpu_steps(oracle, reps)
+        med = statistics.median(rates)
+        return med, threads, (f"{reps} batched decode steps of {rows} sessions (the reference's 64-row "
+                              f"ForwardBatch cap) from this config's layout, greedy; median {med:.0f}, best "
+                              f"{max(rates):.0f} tokens/s; " + baseline_label(oracle, threads))
 
 
 class ServingWorkload:
@@ -750,7 +912,7 @@ def run_beam(args, rank, world, local):
 
 
 def run_prefix(args, rank, world, local):
-    """Primed tool prefix (SURVEY next-row 3): new sessions start on a
+    """Primed tool prefix (primed-prefix export/import and page sharing): new sessions start on a
     384-token primed prefix of the cfg2 decoder (12 layers, d 512) and decode
     their first token, 64 sessions per step, three ways: sharing the primed
     slot's KV pages (ndl_slot_share_prefix: whole pages by reference, the
@@ -844,6 +1006,58 @@ def run_prefix(args, rank, world, local):
     eng.close()
 
 
+# ----------------------------------------------------------------- cases --
+# Small, self-contained cases for kernel captures under a profiler
+# (python bench.py --case attention | --case gemm M N K); they print the
+# device times and no benchmark line.
+#  attention: a 2-layer synthetic decoder with the cfg5 batch shape (512
+#    rows, 8 heads, prefixes U[64,1024]), so each attention launch has the
+#    full-size shape while the engine holds ~1.3 GB of KV pages instead of 12
+#    layers' worth; 4 profiled steps.
+#  gemm M N K: five calls of the I8G32 linear on random int8 activations and
+#    weights with fp16 group scales (M >= 64: the tcgen05 GEMM, else the GEMV).
+
+def case_attention(steps=4, rows=512, seed=5):
+    entry.load_package()
+    from needle_cs_b200.engine import BatchedEngine, SyntheticDecoder
+
+    eng = BatchedEngine(SyntheticDecoder(layers=2, seed=1), slots=rows, context_length=1088, chunk_size=512,
+                        max_heads=rows)
+    lengths = np.random.default_rng(seed).integers(64, 1025, rows)
+    for j in range(rows):
+        eng.fill_synthetic(j, int(lengths[j]), seed, j)
+    tokens = np.random.default_rng(seed + 1).integers(0, 8192, rows).astype(np.int32)
+    order = np.arange(rows, dtype=np.int32)
+    eng.profile(True)
+    for _ in range(steps):
+        eng.forward_batch(tokens, order, order)
+        tokens = eng.sample_argmax()
+    eng.sync()
+    prof = eng.profile_read()
+    eng.close()
+    print({k: (round(v[0], 3), v[1]) for k, v in prof.items()})
+
+
+def case_gemm(m, n, k, calls=5):
+    import torch
+
+    entry.load_package()
+    import importlib
+
+    ops = importlib.import_module("needle_cs_b200.ops")
+    dev = torch.device("cuda:0")
+    q = torch.randint(-128, 128, (m, k), dtype=torch.int8, device=dev)
+    sa = torch.rand(m, device=dev) * 0.01
+    w = torch.randint(-127, 128, (n, k), dtype=torch.int8, device=dev)
+    sw = torch.full((n, k // 32), 0x2000, dtype=torch.int16, device=dev)
+    y = torch.empty((m, n), device=dev)
+    for _ in range(calls):
+        ops.matmul_i8g32(q, sa, w, sw, y=y)
+    torch.cuda.synchronize()
+    print("gemm", m, n, k, "ok")
+
+
+
 WORKLOADS = {"cfg1": GemvWorkload, "cfg2": DecodeWorkload, "cfg3": ServingWorkload, "cfg4": BeamWorkload,
              "cfg5": DecodeWorkload, "prefix": None, "cq": CqWorkload}
 DECODE = ("cfg2", "cfg5")
@@ -856,31 +1070,41 @@ def make_workload(name, args):
 
 
 def run_reference(args, rank, world):
-    """CPU restatement of the reference algorithm on the host cores."""
+    """The reference's CPU algorithms on the host cores: for the decode
+    workloads and cfg1 the AVX2 restatement (oracle/avx2_decoder.c), built
+    from the oracle's own generator so the CUDA library is never loaded; the
+    serving and beam workloads replay on the scalar restatement."""
     if rank != 0:
         return
     oracle = entry.load_oracle()
-    entry.load_package()
     wl = make_workload(args.workload, args)
-    wl.ops = __import__("needle_cs_b200.ops", fromlist=["ops"])
-    per_step = []
     if args.workload == "cfg3":
+        entry.load_package()
+        wl.ops = __import__("needle_cs_b200.ops", fromlist=["ops"])
         arrivals, prompts, outs, _ = wl.trace(0)
         value, cores, sample = wl.cpu_sample(oracle, arrivals, prompts, outs)
         metric, unit = "serving output tokens/sec/box", "tokens/s"
     elif args.workload == "cfg4":
+        entry.load_package()
         value, cores, sample = wl.cpu_sample(oracle)
         metric, unit = "beam decode tokens/sec/box", "tokens/s"
     elif args.workload in DECODE:
-        for i in range(max(1, args.steps // 10)):
-            v, cores, sample = wl.cpu_sample(oracle)
-            per_step.append(v)
-        value = statistics.median(per_step)
+        # each of the K timed steps is one batched decode step of 64 sessions
+        rates, cores, rows = wl.cpu_steps(oracle, args.steps, warmup=args.warmup)
+        value = len(rates) * rows / sum(rows / r for r in rates)
+        sample = (f"{len(rates)} timed batched decode steps of {rows} sessions (the reference's 64-row "
+                  f"ForwardBatch cap) after {args.warmup} warm-up steps; median {statistics.median(rates):.0f}, "
+                  f"best {max(rates):.0f} tokens/s; " + baseline_label(oracle, cores))
         metric, unit = DECODE_METRIC, "tokens/s"
+    elif args.workload == "cfg1":
+        value, cores, sample = wl.cpu_sample(oracle, budget_s=3.0, reps=max(5, args.steps))
+        metric, unit = LINEAR_METRIC, "GB/s"
     else:
-        cores = 1
+        entry.load_package()
+        wl.ops = __import__("needle_cs_b200.ops", fromlist=["ops"])
+        per_step = []
         for i in range(args.warmup + args.steps):
-            v, sample = wl.cpu_sample(oracle, budget_s=3.0)
+            v, cores, sample = wl.cpu_sample(oracle, budget_s=3.0)
             if i >= args.warmup:
                 per_step.append(v)
         value = statistics.median(per_step)
@@ -915,8 +1139,10 @@ def run_decode(args, rank, world, local):
         t_begin = torch.cuda.Event(enable_timing=True)
         t_end = torch.cuda.Event(enable_timing=True)
         t_begin.record(wl.stream)
+        host_t0 = time.perf_counter()
         for _ in range(args.steps):
             launches += wl.step(timed=True)
+        host_ms = (time.perf_counter() - host_t0) * 1e3
         t_end.record(wl.stream)
         torch.cuda.synchronize()
     for e in engines:
@@ -943,8 +1169,13 @@ def run_decode(args, rank, world, local):
         e.profile(False)
     prof_attn_bytes = wl.attn_bytes
     wl.attn_bytes, wl.spans = attn_bytes_main, spans_main
-    dev_ms = max_over_ranks(wl.device_ms(), world)
-    wall_ms = max_over_ranks(t_begin.elapsed_time(t_end), world)
+    my_dev_ms, my_wall_ms = wl.device_ms(), t_begin.elapsed_time(t_end)
+    # per rank: device ms of the steps, event-timed wall ms (device time plus
+    # the gaps between steps while the host reads the ids and issues the
+    # next step) and host ms of the loop, all per step
+    ranks = gather_ranks([my_dev_ms / args.steps, my_wall_ms / args.steps, host_ms / args.steps], world)
+    dev_ms = max_over_ranks(my_dev_ms, world)
+    wall_ms = max_over_ranks(my_wall_ms, world)
     ms_per_step = dev_ms / args.steps
     value = world * wl.units_per_step() * args.steps / (dev_ms * 1e-3)
     e2e_value = world * wl.units_per_step() * args.steps / (wall_ms * 1e-3)
@@ -990,7 +1221,12 @@ def run_decode(args, rank, world, local):
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": 3 * wl.sessions * 4,
                     "d2h_bytes_per_step": wl.sessions * 4, "ms_per_step": wall_ms / args.steps},
             "gpu_launches": launches,
-            "clocks": clocks.summary()}
+            "clocks": clocks.summary(),
+            "ranks": [{"rank": r, "device_ms_per_step": round(v[0], 4), "wall_ms_per_step": round(v[1], 4),
+                       "gap_ms_per_step": round(v[1] - v[0], 4), "host_ms_per_step": round(v[2], 4)}
+                      for r, v in enumerate(ranks)]}
+    if rank == 0 and world == 1:
+        line["gemv"], line["gemm"] = linear_records(device)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         oracle = entry.load_oracle()
         v, cores, sample = wl.cpu_sample(oracle)
@@ -1070,8 +1306,8 @@ def run_ours(args, rank, world, local):
             "clocks": clocks.summary()}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         oracle = entry.load_oracle()
-        v, sample = wl.cpu_sample(oracle)
-        line["cpu_baseline"] = {"value": v, "unit": "GB/s", "cores": 1, "kind": "port", "sample": sample}
+        v, cores, sample = wl.cpu_sample(oracle)
+        line["cpu_baseline"] = {"value": v, "unit": "GB/s", "cores": cores, "kind": "port", "sample": sample}
     if rank == 0:
         print(json.dumps(line), flush=True)
 
@@ -1085,7 +1321,17 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="cfg5")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--case", nargs="+", metavar="CASE",
+                    help="run a profiling case instead: attention | gemm M N K")
     args = ap.parse_args()
+    if args.case:
+        if args.case[0] == "attention":
+            case_attention()
+        elif args.case[0] == "gemm" and len(args.case) == 4:
+            case_gemm(*(int(v) for v in args.case[1:4]))
+        else:
+            raise SystemExit(f"unknown case {args.case!r}")
+        return
     if args.warmup < 3:
         args.warmup = 3
     rank, world, local = (int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")),

@@ -86,6 +86,54 @@ uint16_t ndo_half_bits(float value) {
 }
 
 /* ------------------------------------------------------------------------ */
+/* The benchmark configs' synthetic inputs                                   */
+/* ------------------------------------------------------------------------ */
+/* A counter-based generator: value i of stream `stream` under `seed` is a
+ * function of (seed, stream, i) alone.  splitmix64 mixing (Steele, Lea and
+ * Flood, 2014); normal = Irwin-Hall(12) - 6 from twelve 16-bit uniforms,
+ * scaled to unit variance, in exact integer arithmetic; uniform = the top 24
+ * bits of one hash, lo + (hi - lo) * u in float; int8 = hash mod 255 - 127.
+ * The CUDA library generates the engine's weights and prefix caches with the
+ * same definition; these host copies let the CPU baselines and tests build
+ * them without it. */
+static uint64_t splitmix64(uint64_t z) {
+    z += 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+static uint64_t synth_key(uint64_t seed, uint64_t stream) { return splitmix64(seed ^ (stream * 0x9E3779B97F4A7C15ull)); }
+static uint64_t synth_hash(uint64_t key, uint64_t i) { return splitmix64(key + i * 0xD1B54A32D192ED03ull); }
+static int sum16x4(uint64_t h) {
+    return (int)(h & 0xFFFF) + (int)((h >> 16) & 0xFFFF) + (int)((h >> 32) & 0xFFFF) + (int)(h >> 48);
+}
+
+void ndo_synth_normal(uint64_t seed, uint64_t stream, uint64_t first, size_t count, float scale, float *out) {
+    const uint64_t key = synth_key(seed, stream);
+    for (size_t n = 0; n < count; n++) {
+        const uint64_t i = first + n;
+        const int s = sum16x4(synth_hash(key, 3 * i)) + sum16x4(synth_hash(key, 3 * i + 1)) +
+                      sum16x4(synth_hash(key, 3 * i + 2));
+        out[n] = ((float)(2 * s - 786420) * (1.0f / 131072.0f)) * scale;
+    }
+}
+
+void ndo_synth_uniform(uint64_t seed, uint64_t stream, uint64_t first, size_t count, float lo, float hi, float *out) {
+    const uint64_t key = synth_key(seed, stream);
+    for (size_t n = 0; n < count; n++) {
+        const float u = (float)(synth_hash(key, first + n) >> 40) * (1.0f / 16777216.0f);
+        const float span = hi - lo;
+        const float t = span * u;
+        out[n] = lo + t;
+    }
+}
+
+void ndo_synth_int8(uint64_t seed, uint64_t stream, uint64_t first, size_t count, int8_t *out) {
+    const uint64_t key = synth_key(seed, stream);
+    for (size_t n = 0; n < count; n++) out[n] = (int8_t)((int)(synth_hash(key, first + n) % 255u) - 127);
+}
+
+/* ------------------------------------------------------------------------ */
 /* Row primitives: src/Needle/Scalar.cs                                      */
 /* ------------------------------------------------------------------------ */
 

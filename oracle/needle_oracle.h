@@ -38,6 +38,11 @@ void ndo_fill_sbyte(int8_t *x, int n, uint64_t *state, int extremes);
 void ndo_fill_bytes(uint8_t *x, int n, uint64_t *state, int extremes);
 uint16_t ndo_half_bits(float value);
 
+/* ---- the benchmark configs' synthetic inputs (counter-based generator) ---- */
+void ndo_synth_normal(uint64_t seed, uint64_t stream, uint64_t first, size_t count, float scale, float *out);
+void ndo_synth_uniform(uint64_t seed, uint64_t stream, uint64_t first, size_t count, float lo, float hi, float *out);
+void ndo_synth_int8(uint64_t seed, uint64_t stream, uint64_t first, size_t count, int8_t *out);
+
 /* ---- the exponential (MathF.Exp) over an array ---- */
 void ndo_exp_rn(const float *x, int n, float *y);
 void ndo_exp_simd(const float *x, int n, float *y);
@@ -189,6 +194,22 @@ int ndo_decoder_row_cross(const ndo_decoder *m, int token, int pos, int capacity
  * with scales ks/vs [frames][heads]. */
 int ndo_cross_memory(const ndo_decoder *m, int layer, const float *memory, int frames, int8_t *k, int8_t *v, float *ks,
                      float *vs);
+
+/* ---- the AVX2 CPU baseline (avx2_decoder.c) ---- */
+typedef struct ndb_model ndb_model;
+ndb_model *ndb_model_create(const ndo_decoder *m);
+void ndb_model_destroy(ndb_model *b);
+/* rows decode tokens[r] at pos[r] of their own caches (kv_k[r] etc.);
+ * logits [rows][vocab]; equal to ndo_decoder_row per row, bit for bit. */
+int ndb_decode_step(const ndb_model *b, int rows, const int32_t *tokens, const int32_t *pos, int capacity,
+                    int8_t *const *kv_k, int8_t *const *kv_v, float *const *kv_ks, float *const *kv_vs,
+                    const float *rope_cos, const float *rope_sin, float *logits, int threads);
+/* the int8 linear alone: ndo_matmul_i8g32's y, bit for bit */
+void ndb_matmul_i8g32(const int8_t *w, const uint16_t *sw, int n, int k, const int8_t *q, const float *sa, int m,
+                      float *y, int ldy, int threads);
+void *ndb_linear_create(const int8_t *w, const uint16_t *sw, int n, int k);
+void ndb_linear_run(const void *linear, const int8_t *q, const float *sa, int m, float *y, int ldy, int threads);
+void ndb_linear_destroy(void *linear);
 
 #ifdef __cplusplus
 }

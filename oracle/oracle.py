@@ -77,6 +77,16 @@ _SIGS = {
     "ndo_decoder_row": (I, [P, I, I, I, P, P, P, P, P, P, P]),
     "ndo_decoder_row_cross": (I, [P, I, I, I, P, P, P, P, P, P, I, P, P, P, P, P]),
     "ndo_cross_memory": (I, [P, I, P, I, P, P, P, P]),
+    "ndo_synth_normal": (None, [U64, U64, U64, _c.c_size_t, F, P]),
+    "ndo_synth_uniform": (None, [U64, U64, U64, _c.c_size_t, F, F, P]),
+    "ndo_synth_int8": (None, [U64, U64, U64, _c.c_size_t, P]),
+    "ndb_model_create": (P, [P]),
+    "ndb_model_destroy": (None, [P]),
+    "ndb_decode_step": (I, [P, I, P, P, I, P, P, P, P, P, P, P, I]),
+    "ndb_matmul_i8g32": (None, [P, P, I, I, P, P, I, P, I, I]),
+    "ndb_linear_create": (P, [P, P, I, I]),
+    "ndb_linear_run": (None, [P, P, P, I, P, I, I]),
+    "ndb_linear_destroy": (None, [P]),
 }
 
 _lib = None
@@ -506,3 +516,162 @@ def beam_search(dec, memory, prompt, width, max_steps, eos, length_penalty=1.0, 
         if v > best_score:
             best, best_score = toks, v
     return (best or []), float(best_score)
+
+
+# ---------------------------------------------------------------- AVX2 --
+# The CPU baseline (oracle/avx2_decoder.c): the reference's AVX2 kernels'
+# algorithms on all host cores, equal to the scalar restatement bit for bit.
+
+def host_threads():
+    """Threads for the CPU baseline: NEEDLE_THREADS when set (the reference's
+    thread-count variable), else every host core."""
+    return int(os.environ.get("NEEDLE_THREADS", "0")) or os.cpu_count() or 1
+
+
+def matmul_i8g32_avx2(q, sa, w, sw, threads=None):
+    q = np.ascontiguousarray(q, np.int8)
+    sa = f32(sa)
+    w = np.ascontiguousarray(w, np.int8)
+    sw = np.ascontiguousarray(sw, np.uint16)
+    m, k = q.shape
+    n = w.shape[0]
+    y = np.empty((m, n), np.float32)
+    lib().ndb_matmul_i8g32(ptr(w), ptr(sw), n, k, ptr(q), ptr(sa), m, ptr(y), n, threads or host_threads())
+    return y
+
+
+class AVX2Linear:
+    """A prepared int8 linear for repeated timing."""
+
+    def __init__(self, w, sw):
+        self.w = np.ascontiguousarray(w, np.int8)
+        self.sw = np.ascontiguousarray(sw, np.uint16)
+        self.n, self.k = self.w.shape
+        self.h = lib().ndb_linear_create(ptr(self.w), ptr(self.sw), self.n, self.k)
+        if not self.h:
+            raise MemoryError("AVX2 linear allocation failed")
+
+    def run(self, q, sa, y, threads=None):
+        lib().ndb_linear_run(self.h, ptr(q), ptr(sa), q.shape[0], ptr(y), y.shape[1], threads or host_threads())
+
+    def close(self):
+        if self.h:
+            lib().ndb_linear_destroy(self.h)
+            self.h = None
+
+
+class AVX2Decoder:
+    """The decoder's batched decode step on the CPU with AVX2 and all host
+    cores (ndb_decode_step), over the tensors of an oracle Decoder."""
+
+    def __init__(self, dec):
+        self.dec = dec
+        self.h = lib().ndb_model_create(_c.byref(dec.s))
+        if not self.h:
+            raise MemoryError("AVX2 model allocation failed")
+
+    def step(self, tokens, positions, kvs, threads=None):
+        """tokens/positions [rows]; kvs: one new_kv() dict per row.  Writes
+        each row's K/V at its position and returns logits [rows][vocab]."""
+        rows = len(tokens)
+        t = np.ascontiguousarray(tokens, np.int32)
+        p = np.ascontiguousarray(positions, np.int32)
+        arrs = {key: (P * rows)(*[kv[key].ctypes.data for kv in kvs]) for key in ("k", "v", "ks", "vs")}
+        logits = np.empty((rows, self.dec.cfg.vocab), np.float32)
+        st = lib().ndb_decode_step(self.h, rows, ptr(t), ptr(p), self.dec.capacity, arrs["k"], arrs["v"],
+                                   arrs["ks"], arrs["vs"], ptr(self.dec.cos), ptr(self.dec.sin), ptr(logits),
+                                   threads or host_threads())
+        if st != 0:
+            raise MemoryError("AVX2 step scratch allocation failed")
+        return logits
+
+    def close(self):
+        if self.h:
+            lib().ndb_model_destroy(self.h)
+            self.h = None
+
+
+# ------------------------------------------------------------ synthetic --
+# The benchmark configs' inputs built on the host by the oracle's own copy of
+# the generator (no CUDA library involved): the synthetic decoder's tensors
+# and the prefix K/V of its sessions.  Stream ids under the model seed:
+# embedding 1, final norm 2, layer l field f at 100 + 16*l + f (w_qkv, s_qkv,
+# w_o, s_o, w_gu, s_gu, w_d, s_d, attn_norm, ffn_norm); weights U{-127..127},
+# scales fp16 U(0.001, 0.02), norms 1 + 0.1*normal, the embedding fp16
+# 0.02*normal, the head int8 quantized from the embedding per (row, 32-group).
+
+def synth_normal(seed, stream, count, scale=1.0, first=0):
+    out = np.empty(count, np.float32)
+    lib().ndo_synth_normal(seed, stream, first, count, scale, ptr(out))
+    return out
+
+
+def synth_normal_f16(seed, stream, count, scale=1.0, first=0):
+    """fp16 bits (IEEE round to nearest even) of normal * scale."""
+    return synth_normal(seed, stream, count, scale, first).astype(np.float16).view(np.uint16)
+
+
+def synth_uniform_f16(seed, stream, count, lo, hi, first=0):
+    out = np.empty(count, np.float32)
+    lib().ndo_synth_uniform(seed, stream, first, count, lo, hi, ptr(out))
+    return out.astype(np.float16).view(np.uint16)
+
+
+def synth_int8(seed, stream, count, first=0):
+    out = np.empty(count, np.int8)
+    lib().ndo_synth_int8(seed, stream, first, count, ptr(out))
+    return out
+
+
+class DecoderConfig:
+    """The synthetic decoder's shape (defaults: the 12-layer decoder of
+    configs 2, 3 and 5)."""
+
+    def __init__(self, layers=12, dim=512, heads=8, head_dim=64, ffn=2048, vocab=8192, rope_theta=10000.0, seed=1):
+        self.layers, self.dim, self.heads, self.head_dim = layers, dim, heads, head_dim
+        self.ffn, self.vocab, self.rope_theta, self.seed, self.cross = ffn, vocab, rope_theta, seed, 0
+
+
+_FIELDS = ["w_qkv", "s_qkv", "w_o", "s_o", "w_gu", "s_gu", "w_d", "s_d", "attn_norm", "ffn_norm"]
+
+
+def synthetic_decoder(cfg, capacity):
+    """An oracle Decoder over the synthetic decoder's tensors."""
+    seed, d, F, V = cfg.seed, cfg.dim, cfg.ffn, cfg.vocab
+    G, GF = d // 32, F // 32
+    shapes = {"w_qkv": (3 * d * d, "i8"), "s_qkv": (3 * d * G, "s"), "w_o": (d * d, "i8"), "s_o": (d * G, "s"),
+              "w_gu": (2 * F * d, "i8"), "s_gu": (2 * F * G, "s"), "w_d": (d * F, "i8"), "s_d": (d * GF, "s"),
+              "attn_norm": (d, "n"), "ffn_norm": (d, "n")}
+
+    def gen(name, stream):
+        count, kind = shapes[name]
+        if kind == "i8":
+            return synth_int8(seed, stream, count)
+        if kind == "s":
+            return synth_uniform_f16(seed, stream, count, 0.001, 0.02)
+        return (np.float32(1.0) + np.float32(0.1) * synth_normal(seed, stream, count)).astype(np.float32)
+
+    layers = [{name: gen(name, 100 + 16 * l + f) for f, name in enumerate(_FIELDS)} for l in range(cfg.layers)]
+    final_norm = (np.float32(1.0) + np.float32(0.1) * synth_normal(seed, 2, d)).astype(np.float32)
+    emb = synth_normal_f16(seed, 1, V * d, scale=0.02)
+    e = emb.view(np.float16).astype(np.float32).reshape(V, d // 32, 32)
+    peak = np.abs(e).max(axis=2)
+    s16 = np.where(peak > 0, peak / np.float32(127.0), np.float32(1.0)).astype(np.float32).astype(np.float16)
+    inv = (np.float32(1.0) / s16.astype(np.float32)).astype(np.float32)
+    w_head = np.clip(np.rint(e * inv[:, :, None]), -127, 127).astype(np.int8).reshape(-1)
+    s_head = s16.view(np.uint16).reshape(-1)
+    return Decoder(cfg, layers, final_norm, emb, w_head, s_head, capacity)
+
+
+def synthetic_prefix_kv(dec, kv, count, seed, session):
+    """Positions [0, count) of a session's cache: fp16 N(0,1) K and V from
+    (seed, session) at index ((((layer*2 + kind) << 20) + pos) * heads +
+    head) * 64 + d, quantized per (position, head) (QuantizeInt8)."""
+    H = dec.cfg.heads
+    for layer in range(dec.cfg.layers):
+        for kind, (vals, scales) in enumerate((("k", "ks"), ("v", "vs"))):
+            first = ((layer * 2 + kind) << 20) * H * 64
+            raw = synth_normal_f16(seed, session, count * H * 64, first=first)
+            q, sc = quantize_rows(raw.view(np.float16).astype(np.float32).reshape(count * H, 64))
+            kv[vals][layer, :count] = q.reshape(count, H * 64)
+            kv[scales][layer, :count] = sc.reshape(count, H)

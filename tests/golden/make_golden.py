@@ -86,7 +86,9 @@ CSHARP_ASSERTS = {
 
 
 def main(argv):
-    root = argv[1] if len(argv) > 1 else os.environ.get("NEEDLE_CS_ROOT", "/root/reference")
+    if len(argv) < 2:
+        raise SystemExit("usage: make_golden.py NEEDLE_CS_SOURCE_TREE  (the needle-cs checkout to read fixtures from)")
+    root = argv[1]
     fixtures, entries = load_reference_fixtures(root)
     doc = {
         "generated_by": "tests/golden/make_golden.py",
