@@ -191,15 +191,16 @@ constexpr int kAttnPageRegs = kAttnMaxPositions / kPagePositions / 32;  // page 
 constexpr uint32_t kWaitLimit = 1u << 22;
 
 // Shared memory of one CTA for rows of at most max_pages pages: per warp
-// [ring stages][64 PV weights][stage page flags][scores], then the
-// barriers full[warp][stage].
+// [ring stages][64 PV weights][64 exponentials][stage page flags][scores],
+// then the barriers full[warp][stage].
 struct AttnSmem {
-    int wbuf, flags, scores, warp_bytes, bars, total;
+    int wbuf, ebuf, flags, scores, warp_bytes, bars, total;
 };
 __host__ __device__ __forceinline__ AttnSmem attn_smem(int max_pages) {
     AttnSmem s;
     s.wbuf = kAttnStages * kKvHalfBytes;
-    s.flags = s.wbuf + kPagePositions * 4;
+    s.ebuf = s.wbuf + kPagePositions * 4;
+    s.flags = s.ebuf + kPagePositions * 4;
     s.scores = s.flags + 16;
     s.warp_bytes = s.scores + max_pages * kPagePositions * 4;
     s.bars = kAttnWarps * s.warp_bytes;
@@ -240,25 +241,6 @@ __global__ void __launch_bounds__(128) attn_work_kernel(AttnArgs a) {
     if (!valid)
         for (int t = threadIdx.x; t < a.heads * kHeadDim; t += blockDim.x)
             a.out[(size_t)row * a.heads * kHeadDim + t] = __int_as_float(0x7fc00000);
-}
-
-// ExponentiateAcrossPositions' total (src/Needle/Blocks.cs:381-404): four
-// partial sums by position modulo 4 over the whole quads, the positions past
-// the last quad added to the first, combined as (s0 + s1) + (s2 + s3).
-// Lanes 0..3 keep one partial each; every lane returns the total.
-__device__ __forceinline__ float total_four_way(const float *e, int n, int lane) {
-    const int quads = n >> 2;
-    float t = 0.0f;
-    if (lane < 4) {
-#pragma unroll 4
-        for (int i = 0; i < quads; i++) t = __fadd_rn(t, e[4 * i + lane]);
-        if (lane == 0)
-            for (int j = 4 * quads; j < n; j++) t = __fadd_rn(t, e[j]);
-    }
-    const float s1 = __shfl_sync(0xffffffffu, t, 1), s2 = __shfl_sync(0xffffffffu, t, 2),
-                s3 = __shfl_sync(0xffffffffu, t, 3);
-    const float total = __fadd_rn(__fadd_rn(t, s1), __fadd_rn(s2, s3));
-    return __shfl_sync(0xffffffffu, total, 0);
 }
 
 // One 16-position chunk of pass B for the lane's two dims: va / vb hold the
@@ -379,11 +361,13 @@ __device__ __forceinline__ void attn_issue(const AttnArgs &a, uint8_t *wsm, int 
 //    cores (mma.sync m16n8k32 s8, K as A, the query in every B column; lane
 //    (gid, tig) keeps positions 16*tig + gid and + 8), then
 //    s = (dot * ks) * (qs / sqrt(d)) into the warp's score buffer;
-//  * softmax as the AVX2 tier: max, e = Ops.Exp(s - max) per position,
-//    their total in four partial sums by position modulo 4, 1 / total;
-//  * pass B: weights w = e * vs per position, then acc[d] = fma(w, v[d],
-//    acc[d]) in position order, two dims (lane, lane + 32) per lane;
-//    out = acc * (1 / total).
+//  * the max over the row's scores;
+//  * pass B, page by page: e = Ops.Exp(s - max) for every position, the four
+//    partial sums of e by position modulo 4 (lanes 0..3), weights
+//    w = e * vs, then acc[d] = fma(w, v[d], acc[d]) in position order, two
+//    dims (lane, lane + 32) per lane; at the end out = acc * (1 / total)
+//    with total = (s0 + s1) + (s2 + s3).  The total is needed only then, so
+//    no separate softmax pass sits between the two.
 // The next item's claim, record and query are loaded into registers while
 // the current one computes, each used only a phase after its load was issued.
 __global__ void __launch_bounds__(kAttnThreads, 3) attn_decode_kernel(AttnArgs a) {
@@ -393,6 +377,7 @@ __global__ void __launch_bounds__(kAttnThreads, 3) attn_decode_kernel(AttnArgs a
     const int gid = lane >> 2, tig = lane & 3;
     uint8_t *wsm = smem + (size_t)warp * L.warp_bytes;
     float *wbuf = reinterpret_cast<float *>(wsm + L.wbuf);
+    float *ebuf = reinterpret_cast<float *>(wsm + L.ebuf);
     int *flags = reinterpret_cast<int *>(wsm + L.flags);
     float *sc = reinterpret_cast<float *>(wsm + L.scores);
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + L.bars) + warp * kAttnStages;
@@ -477,16 +462,17 @@ __global__ void __launch_bounds__(kAttnThreads, 3) attn_decode_kernel(AttnArgs a
         if (timed_out) break;
         // the next item's record (the claim has long returned)
         item_fetch_record(a, __shfl_sync(0xffffffffu, claim, 0), n_work, lane, nx);
-        // ---- softmax (Normalizers, ExponentiateAcrossPositions): e = Ops.Exp(s - peak) ----
         peak = warp_max_f(peak);
         __syncwarp();
-        for (int j = lane; j < len; j += 32) sc[j] = exp_simd(__fsub_rn(sc[j], peak));
-        __syncwarp();
-        const float inverse = __fdiv_rn(1.0f, total_four_way(sc, len, lane));
         item_fetch_query(a, lane, nx);
         next_ready = true;
-        // ---- pass B (ValuesFloat, AccumulateFloat): acc[d] = fma(e_j * vs_j, v_j[d], acc[d]) ----
+        // ---- pass B: per page e = Ops.Exp(s - peak) (ExponentiateAcrossPositions), the four
+        // partial sums by position modulo 4 on lanes 0..3 (positions past the last whole quad
+        // go to the first, in order), w = e * vs (ValuesFloat), acc[d] = fma(w, v[d], acc[d])
+        // (AccumulateFloat) ----
         uint64_t acc = f2_pack(0.0f, 0.0f);  // dims lane, lane + 32
+        const int quads = len & ~3;           // positions summed four ways
+        float part = 0.0f;                    // lane k < 4: partial sum k
         for (int pg = 0; pg < n_pages; pg++) {
             const int stage = st.consumed % kAttnStages;
             if (!mbar_wait_bounded(&full[stage], (st.consumed / kAttnStages) & 1, kWaitLimit)) {
@@ -497,8 +483,13 @@ __global__ void __launch_bounds__(kAttnThreads, 3) attn_decode_kernel(AttnArgs a
             const float *vs = reinterpret_cast<const float *>(blk);
             const int valid = min(kPagePositions, len - pg * kPagePositions);
             // positions past the row's end get weight 0: fma(0, v, acc) is acc
-            wbuf[lane] = lane < valid ? __fmul_rn(sc[pg * kPagePositions + lane], vs[lane]) : 0.0f;
-            wbuf[lane + 32] = lane + 32 < valid ? __fmul_rn(sc[pg * kPagePositions + lane + 32], vs[lane + 32]) : 0.0f;
+            const float e0 = lane < valid ? exp_simd(__fsub_rn(sc[pg * kPagePositions + lane], peak)) : 0.0f;
+            const float e1 =
+                lane + 32 < valid ? exp_simd(__fsub_rn(sc[pg * kPagePositions + lane + 32], peak)) : 0.0f;
+            ebuf[lane] = e0;
+            ebuf[lane + 32] = e1;
+            wbuf[lane] = __fmul_rn(e0, vs[lane]);
+            wbuf[lane + 32] = __fmul_rn(e1, vs[lane + 32]);
             uint4 va[4], vb[4];
 #pragma unroll
             for (int ch = 0; ch < 4; ch++) {
@@ -512,10 +503,22 @@ __global__ void __launch_bounds__(kAttnThreads, 3) attn_decode_kernel(AttnArgs a
             attn_issue(a, wsm, flags, full, st, cur, nx, next_ready, lane);
 #pragma unroll
             for (int ch = 0; ch < 4; ch++) acc = pv_chunk(acc, va[ch], vb[ch], wbuf + 16 * ch);
-            __syncwarp();  // the weights are read before the next page rewrites them
+            if (lane < 4) {
+                const int base = pg * kPagePositions;
+#pragma unroll 4
+                for (int i = 0; i < 16; i++)
+                    if (base + 4 * i + lane < quads) part = __fadd_rn(part, ebuf[4 * i + lane]);
+                if (lane == 0)
+                    for (int p = max(quads, base); p < base + valid; p++) part = __fadd_rn(part, ebuf[p - base]);
+            }
+            __syncwarp();  // the weights and exponentials are read before the next page rewrites them
         }
         if (timed_out) break;
         float *out = a.out + ((size_t)cur.row * a.heads + cur.head) * kHeadDim;
+        const float s1 = __shfl_sync(0xffffffffu, part, 1), s2 = __shfl_sync(0xffffffffu, part, 2),
+                    s3 = __shfl_sync(0xffffffffu, part, 3);
+        const float inverse =
+            __shfl_sync(0xffffffffu, __fdiv_rn(1.0f, __fadd_rn(__fadd_rn(part, s1), __fadd_rn(s2, s3))), 0);
         float acc_a, acc_b;
         f2_unpack(acc, acc_a, acc_b);
         const float nan = __int_as_float(0x7fc00000);
