@@ -488,8 +488,9 @@ __global__ void __launch_bounds__(kAttnThreads, 3) attn_decode_kernel(AttnArgs a
                 lane + 32 < valid ? exp_simd(__fsub_rn(sc[pg * kPagePositions + lane + 32], peak)) : 0.0f;
             ebuf[lane] = e0;
             ebuf[lane + 32] = e1;
-            wbuf[lane] = __fmul_rn(e0, vs[lane]);
-            wbuf[lane + 32] = __fmul_rn(e1, vs[lane + 32]);
+            // (the V scales of positions past the row's end are stale page bytes: never multiplied)
+            wbuf[lane] = lane < valid ? __fmul_rn(e0, vs[lane]) : 0.0f;
+            wbuf[lane + 32] = lane + 32 < valid ? __fmul_rn(e1, vs[lane + 32]) : 0.0f;
             uint4 va[4], vb[4];
 #pragma unroll
             for (int ch = 0; ch < 4; ch++) {
