@@ -1222,7 +1222,7 @@ def run_decode(args, rank, world, local):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "int8xint8->int32,f32", "data": "synthetic",
             "config": wl.describe(),
-            "roofline": {"bound": "hbm", "kernel": "attn_decode_kernel (paged int8 KV, split-K)",
+            "roofline": {"bound": "hbm", "kernel": "attn_decode_kernel (paged int8 KV, unsplit rows, exact AVX2-tier softmax)",
                          "achieved": attn_achieved, "peak": peak, "unit": "GB/s",
                          "frac": attn_achieved / peak if attn_achieved else None,
                          "traffic": ATTN_TRAFFIC_PER_ALG_BYTE * attn_launch_bytes,
