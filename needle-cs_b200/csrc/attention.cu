@@ -189,6 +189,7 @@ constexpr int kAttnStages = NDL_ATTN_STAGES;  // ring stages (half records) per 
 constexpr int kAttnThreads = 32 * kAttnWarps;
 constexpr int kAttnPageRegs = kAttnMaxPositions / kPagePositions / 32;  // page ids per lane of an item
 constexpr uint32_t kWaitLimit = 1u << 22;
+constexpr int kClaimLead = 4;  // pages of pass B left when a warp claims its next item
 
 // Shared memory of one CTA for rows of at most max_pages pages: per warp
 // [ring stages][64 PV weights][64 exponentials][stage page flags][scores],
@@ -409,8 +410,14 @@ __global__ void __launch_bounds__(kAttnThreads, 3) attn_decode_kernel(AttnArgs a
             st.k_cur = 0;
             continue;
         }
+        // The next item is claimed late, kClaimLead pages before the end of pass B, so a warp commits
+        // to more work only when its current item is nearly done (claims made at an item's start
+        // left the launch's last warps up to a fifth of the kernel behind the others).  Its record
+        // is fetched a page after the claim and used a page after that.  Short items claim at the
+        // start and fetch the record after pass A.
+        const int claim_at = cur.pages >= kClaimLead ? cur.pages - kClaimLead : -1;
         int claim = 0;
-        if (lane == 0) claim = W + atomicAdd(next_item, 1);  // the next item, read after pass A
+        if (claim_at < 0 && lane == 0) claim = W + atomicAdd(next_item, 1);
         bool next_ready = false;
         attn_issue(a, wsm, flags, full, st, cur, nx, next_ready, lane);
         if (!query_ready) item_fetch_query(a, lane, cur);  // lands while the first copies are in flight
@@ -460,12 +467,14 @@ __global__ void __launch_bounds__(kAttnThreads, 3) attn_decode_kernel(AttnArgs a
             }
         }
         if (timed_out) break;
-        // the next item's record (the claim has long returned)
-        item_fetch_record(a, __shfl_sync(0xffffffffu, claim, 0), n_work, lane, nx);
+        if (claim_at < 0)  // a short item: the next item's record (the claim has long returned)
+            item_fetch_record(a, __shfl_sync(0xffffffffu, claim, 0), n_work, lane, nx);
         peak = warp_max_f(peak);
         __syncwarp();
-        item_fetch_query(a, lane, nx);
-        next_ready = true;
+        if (claim_at < 0) {
+            item_fetch_query(a, lane, nx);
+            next_ready = true;
+        }
         // ---- pass B: per page e = Ops.Exp(s - peak) (ExponentiateAcrossPositions), the four
         // partial sums by position modulo 4 on lanes 0..3 (positions past the last whole quad
         // go to the first, in order), w = e * vs (ValuesFloat), acc[d] = fma(w, v[d], acc[d])
@@ -474,6 +483,12 @@ __global__ void __launch_bounds__(kAttnThreads, 3) attn_decode_kernel(AttnArgs a
         const int quads = len & ~3;           // positions summed four ways
         float part = 0.0f;                    // lane k < 4: partial sum k
         for (int pg = 0; pg < n_pages; pg++) {
+            if (pg == claim_at && lane == 0) claim = W + atomicAdd(next_item, 1);
+            if (pg == claim_at + 1) item_fetch_record(a, __shfl_sync(0xffffffffu, claim, 0), n_work, lane, nx);
+            if (pg == claim_at + 2) {
+                item_fetch_query(a, lane, nx);
+                next_ready = true;
+            }
             const int stage = st.consumed % kAttnStages;
             if (!mbar_wait_bounded(&full[stage], (st.consumed / kAttnStages) & 1, kWaitLimit)) {
                 timed_out = true;
@@ -486,8 +501,8 @@ __global__ void __launch_bounds__(kAttnThreads, 3) attn_decode_kernel(AttnArgs a
             const float e0 = lane < valid ? exp_simd(__fsub_rn(sc[pg * kPagePositions + lane], peak)) : 0.0f;
             const float e1 =
                 lane + 32 < valid ? exp_simd(__fsub_rn(sc[pg * kPagePositions + lane + 32], peak)) : 0.0f;
-            ebuf[lane] = e0;
-            ebuf[lane + 32] = e1;
+            ebuf[(lane & 3) * 16 + (lane >> 2)] = e0;
+            ebuf[(lane & 3) * 16 + 8 + (lane >> 2)] = e1;
             // (the V scales of positions past the row's end are stale page bytes: never multiplied)
             wbuf[lane] = lane < valid ? __fmul_rn(e0, vs[lane]) : 0.0f;
             wbuf[lane + 32] = lane + 32 < valid ? __fmul_rn(e1, vs[lane + 32]) : 0.0f;
@@ -506,11 +521,25 @@ __global__ void __launch_bounds__(kAttnThreads, 3) attn_decode_kernel(AttnArgs a
             for (int ch = 0; ch < 4; ch++) acc = pv_chunk(acc, va[ch], vb[ch], wbuf + 16 * ch);
             if (lane < 4) {
                 const int base = pg * kPagePositions;
-#pragma unroll 4
-                for (int i = 0; i < 16; i++)
-                    if (base + 4 * i + lane < quads) part = __fadd_rn(part, ebuf[4 * i + lane]);
-                if (lane == 0)
-                    for (int p = max(quads, base); p < base + valid; p++) part = __fadd_rn(part, ebuf[p - base]);
+                const float *el = ebuf + lane * 16;  // positions base + 4 i + lane, i ascending
+                if (base + kPagePositions <= quads) {
+#pragma unroll
+                    for (int i = 0; i < 16; i += 4) {
+                        const float4 e4 = *reinterpret_cast<const float4 *>(el + i);
+                        part = __fadd_rn(part, e4.x);
+                        part = __fadd_rn(part, e4.y);
+                        part = __fadd_rn(part, e4.z);
+                        part = __fadd_rn(part, e4.w);
+                    }
+                } else {
+                    for (int i = 0; i < 16; i++)
+                        if (base + 4 * i + lane < quads) part = __fadd_rn(part, el[i]);
+                    if (lane == 0)
+                        for (int p = max(quads, base); p < base + valid; p++) {
+                            const int j = p - base;
+                            part = __fadd_rn(part, ebuf[(j & 3) * 16 + (j >> 2)]);
+                        }
+                }
             }
             __syncwarp();  // the weights and exponentials are read before the next page rewrites them
         }

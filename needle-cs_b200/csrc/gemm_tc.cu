@@ -65,7 +65,13 @@ struct TcShape {
     static constexpr int kSlots = kTcTmemCols / kSlotCols;  // 8 (BT 16) or 4
     static constexpr int kXBytes = BT * kTcBlockK;
     static constexpr int kCols = BT / 2;  // token columns per epilogue thread
+    // groups per TMEM load batch (one wait per batch; two batches in flight):
+    // 32 registers of accumulators per batch
+    static constexpr int kBatch = kCols <= 8 ? 4 : kCols <= 16 ? 2 : 1;
+    static_assert(kGroupsPerSlot % kBatch == 0 && 8 % (2 * kBatch) == 0, "batches tile slots and scale chunks");
 };
+// K groups per tile must fill whole batch pairs (and so whole TMEM slots).
+__host__ __device__ constexpr int tc_group_multiple(int bt) { return bt <= 16 ? 8 : bt <= 32 ? 4 : 2; }
 
 template <int BT>
 struct TcSmem {
@@ -238,10 +244,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             while (st >= n_stages) st -= n_stages, lt++;
         }
     } else {
-        // Epilogue.  Loads run one group ahead of the arithmetic; groups go
-        // in pairs (even: dA, odd: dB; G is even) inside 8-group scale chunks,
-        // so buffers, scale halves and slot boundaries are fixed at compile
-        // time (Q divides 8, so group g sits at slot position (g % 8) % Q).
+        // Epilogue.  TMEM loads go in batches of LG groups, one wait per
+        // batch, the next batch loading while the current one folds: dA
+        // holds batches 0, 2, ... and dB batches 1, 3, ... of each 8-group
+        // scale chunk, so buffers, scale halves and slot positions are fixed
+        // at compile time (LG divides Q and Q divides 8; G is a multiple of
+        // 2 * LG, so every tile ends on a batch pair and a whole slot).
+        constexpr int LG = Sh::kBatch;
         const int quad = warp & 3, c0 = ((warp - kTcEpiWarp0) >> 2) * EC;
         const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)c0;
         const bool vec = p.sw_vec != 0;
@@ -260,20 +269,31 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(&s.acc_empty[lsq % S]);
         };
+        auto load_batch = [&](uint32_t (&d)[LG][EC], int pos) {  // groups at slot positions pos ..
+#pragma unroll
+            for (int i = 0; i < LG; i++) tmem_ld<EC>(slot_addr + (uint32_t)((pos + i) * BT), d[i]);
+        };
+        auto wait_batch = [&](uint32_t (&d)[LG][EC]) {
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < LG; i++)
+#pragma unroll
+                for (int c = 0; c < EC; c++) asm volatile("" : "+r"(d[i][c]));
+        };
         auto scale_row = [&](int tile) {
             const TcTile tn = tc_tile(tile, nblk, tblk);
             const int nn = min(tn.n0 + quad * 32 + lane, p.n - 1);
             return p.sw + (long long)tn.bz * p.sw_stride + (size_t)nn * G;
         };
-        uint32_t dA[EC], dB[EC];
+        uint32_t dA[LG][EC], dB[LG][EC];
         uint4 sc_nx = make_uint4(0u, 0u, 0u, 0u);
         bool ok = my_tiles > 0;
         if (ok) {
             sc_nx = tc_scales8(scale_row(blockIdx.x), 0, G, vec);
             ok = next_slot();
             if (ok) {
-                tmem_ld<EC>(slot_addr, dA);
-                tmem_ld_wait(dA);
+                load_batch(dA, 0);
+                wait_batch(dA);
             }
         }
         for (int lt = 0; lt < my_tiles && ok; lt++) {
@@ -314,26 +334,34 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 if (c8 + 8 < G) sc_nx = tc_scales8(srow, c8 + 8, G, vec);
                 else if (more_tiles) sc_nx = tc_scales8(scale_row(blockIdx.x + (lt + 1) * gridDim.x), 0, G, vec);
 #pragma unroll
-                for (int gi = 0; gi < 8; gi += 2) {
-                    const int g = c8 + gi;
+                for (int bi = 0; bi < 8; bi += 2 * LG) {
+                    const int g = c8 + bi;
                     if (g >= G) break;
-                    // group g is in dA; g + 1 (same slot: its position is odd) loads into dB
-                    tmem_ld<EC>(slot_addr + (uint32_t)(((gi + 1) % Q) * BT), dB);
-                    fold(dA, sc, gi, special, g);
-                    tmem_ld_wait(dB);
-                    // g + 1 ends its slot at an even boundary or at the tile's end
-                    const bool last = g + 2 >= G;
-                    const bool slot_end = (gi + 2) % Q == 0 || last;
-                    if (slot_end) release_slot();
-                    // next into dA: g + 2, or the next tile's group 0
+                    // batch g .. g + LG - 1 is in dA; g + LG .. loads into dB (same tile)
+                    const bool end_a = (bi + LG) % Q == 0;  // dA's batch ends its slot
+                    if (end_a) {
+                        release_slot();
+                        ok = next_slot();
+                    }
+                    if (ok) load_batch(dB, (bi + LG) % Q);
+#pragma unroll
+                    for (int i = 0; i < LG; i++) fold(dA[i], sc, bi + i, special, g + i);
+                    if (!ok) break;
+                    wait_batch(dB);
+                    // dB's batch ends its slot at a multiple of Q, always at the tile's end
+                    const bool last = g + 2 * LG >= G;
+                    const bool end_b = (bi + 2 * LG) % Q == 0;
+                    if (end_b) release_slot();
+                    // next into dA: g + 2 LG, or the next tile's first batch
                     const bool next = !last || more_tiles;
                     if (next) {
-                        if (slot_end) ok = next_slot();
-                        if (ok) tmem_ld<EC>(slot_addr + (uint32_t)(last ? 0 : ((gi + 2) % Q) * BT), dA);
+                        if (end_b) ok = next_slot();
+                        if (ok) load_batch(dA, last ? 0 : (bi + 2 * LG) % Q);
                     }
-                    fold(dB, sc, gi + 1, special, g + 1);
+#pragma unroll
+                    for (int i = 0; i < LG; i++) fold(dB[i], sc, bi + LG + i, special, g + LG + i);
                     if (!ok) break;
-                    if (next) tmem_ld_wait(dA);
+                    if (next) wait_batch(dA);
                 }
             }
             if (!ok) break;
@@ -442,9 +470,12 @@ static int pick_bt(const MatmulArgs &a) {
     const int bts[3] = {16, 32, 64};
     const double rate[3] = {28.0, 36.0, 46.0};
     const long long nblk = (long long)a.batch * ((a.n + kTcBlockN - 1) / kTcBlockN);
-    int best = 16;
+    const int G = a.k >> 5;
+    int best = 0;
     double best_t = 1e300;
     for (int i = 0; i < 3; i++) {
+        if (G % tc_group_multiple(bts[i]) != 0) continue;
+        if (bts[i] == 64 && a.residual) continue;  // 64-token tiles have no residual variant
         const long long tiles = nblk * ((a.m + bts[i] - 1) / bts[i]);
         const long long waves = (tiles + tc_sms() - 1) / tc_sms();
         const double t = (double)waves * std::max(60.0, 128.0 * bts[i] / rate[i]);
@@ -457,14 +488,15 @@ int launch_gemm_i8g32_tc(const MatmulArgs &a, cudaStream_t stream) {
     if (a.m < 64) return NDL_ERR_UNSUPPORTED;
     if (a.w_stride % 16 != 0) return NDL_ERR_UNSUPPORTED;
     const int G = a.k >> 5;
-    if (G % 2 != 0) return NDL_ERR_UNSUPPORTED;  // groups go in pairs
+    if (G % tc_group_multiple(64) != 0) return NDL_ERR_UNSUPPORTED;  // groups go in pairs
     const bool sw_vec = G % 8 == 0 && aligned(a.sw, 16) && (a.sw_stride * 2) % 16 == 0;
     TcParams p{a.m,     a.n, a.k,        a.ldy, a.batch,    a.sa, a.sw, a.sw_stride, a.y_stride, a.y, a.residual,
                a.acc, a.status, sw_vec ? 1 : 0};
     switch (pick_bt(a)) {
-        case 64: return a.residual ? launch_bt<32>(a, p, stream) : launch_bt<64>(a, p, stream);
+        case 64: return launch_bt<64>(a, p, stream);
         case 32: return launch_bt<32>(a, p, stream);
-        default: return launch_bt<16>(a, p, stream);
+        case 16: return launch_bt<16>(a, p, stream);
+        default: return NDL_ERR_UNSUPPORTED;  // no tile fits this K: the GEMV serves it
     }
 }
 

@@ -179,13 +179,29 @@ __global__ void __launch_bounds__(kRowThreads) row_quantize_kernel(const float *
         }
         __syncthreads();
         if (tid == 0) {
+            // the chain of adds is the kernel's critical path: the next four
+            // float4 loads go out before the current sixteen adds
             float ss = 0.0f;
-            for (int i = 0; i < nv; i++) {
-                const float4 q4 = squares[i];
-                ss = __fadd_rn(ss, q4.x);
-                ss = __fadd_rn(ss, q4.y);
-                ss = __fadd_rn(ss, q4.z);
-                ss = __fadd_rn(ss, q4.w);
+            const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+            float4 nxt[4];
+#pragma unroll
+            for (int j = 0; j < 4; j++) nxt[j] = j < nv ? squares[j] : zero;
+            for (int i = 0; i < nv; i += 4) {
+                float4 cur[4];
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    cur[j] = nxt[j];
+                    nxt[j] = i + 4 + j < nv ? squares[i + 4 + j] : zero;
+                }
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    if (i + j < nv) {
+                        ss = __fadd_rn(ss, cur[j].x);
+                        ss = __fadd_rn(ss, cur[j].y);
+                        ss = __fadd_rn(ss, cur[j].z);
+                        ss = __fadd_rn(ss, cur[j].w);
+                    }
+                }
             }
             red[0] = ss;
         }
