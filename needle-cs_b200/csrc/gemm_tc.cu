@@ -28,12 +28,14 @@
 //  * warps 4..11 (epilogue): (TMEM lane quadrant) x (BT / 2 token columns).
 //    Three warps per scheduler leave the issuing warps their share of issue
 //    slots and each epilogue thread up to 168 registers.
-//    TMEM is a ring of slots of min(4, 128 / BT) groups.  Per group a thread
-//    loads the next group's D while it folds the current one,
-//    acc = fma(half(sw[n][g]), float(D), acc), two tokens per packed f32x2
-//    instruction; a slot is released as soon as its last group is in
+//    TMEM is a ring of slots of min(4, 128 / BT) groups.  A thread loads D
+//    in batches of 4 / 2 / 1 groups (BT 16 / 32 / 64: 32 registers each),
+//    one wait per batch, the next batch loading while it folds the current
+//    one, acc = fma(half(sw[n][g]), float(D), acc), two tokens per packed
+//    f32x2 instruction (a load round trip per group, not the fold, set the
+//    pace before); a slot is released as soon as its last group is in
 //    registers, and a finished tile (times the token's activation scale,
-//    plus the residual) is written while the next tile's first group loads.
+//    plus the residual) is written while the next tile's first batch loads.
 // Every wait is bounded; on a timeout the CTA records kStatusTimeout, leaves
 // its loops, frees TMEM and exits.
 #include <cudaTypedefs.h>
