@@ -266,8 +266,9 @@ NDL_API void ndl_kt_gather_row(const ndl_kt_cq *w, int row, float *destination);
  *   Taps3              void(float* taps, int width, float* current, float* destination) slot 13
  *                      (reads current[-2*width .. width))
  *   Sinkhorn4x4        void(float* logits, float* result)                      slot 24
- * Equal to the scalar code bit for bit except GateFakeA8 and Sinkhorn4x4,
- * whose exp is CUDA's expf (tolerance). */
+ * Equal to the scalar code bit for bit (MathF.Exp in GateFakeA8 and
+ * Sinkhorn4x4 is the correctly rounded exponential the CPU oracle computes
+ * in the same double-precision steps). */
 NDL_API void ndl_kt_rms_fake_a8(const float *x, int n, float *destination);
 NDL_API void ndl_kt_centered_rms_fake_a8(const float *x, const float *scale, int n, float *destination);
 NDL_API void ndl_kt_gate_fake_a8(float *x, const float *gate, int n);
@@ -332,7 +333,8 @@ NDL_API void ndl_kt_merge_partials(const float *partials, int count, int heads, 
  * MLP on one token's residual row, updated in place; MlpWeights and MlpBatch
  * in the reference's sequential layouts (src/Needle/Audio.cs:5-27,
  * src/Needle/Blocks.cs:992-1004).  Inner sums in the scalar order; the
- * condition softmax and the SiLU go through expf (tolerance). */
+ * condition softmax and the SiLU take MathF.Exp as the correctly rounded
+ * exponential, so the row equals the scalar code's bit for bit. */
 typedef struct {
     const float *d1, *d2, *b2, *d3, *d4;
     const float *w1a, *w1b, *w2a, *w2b, *w3a, *w3b;
@@ -776,14 +778,14 @@ NDL_API int ndl_model_tokenizer(const ndl_model *m, const void **blob, size_t *b
  * ndl_engram_workspace(m, count) bytes, 256-byte aligned.  The model must be
  * on a device; its tables must tile the input (EngramTables x EngramSub ==
  * Dim) and its key / value matrices be 2-bit Dim x Dim, else
- * NDL_ERR_UNSUPPORTED.  Bars: bit-exact to the scalar chain up to the gate,
- * whose sigmoid goes through CUDA's expf. */
+ * NDL_ERR_UNSUPPORTED.  Bit-exact to the scalar chain, the gate's sigmoid
+ * included (MathF.Exp as the correctly rounded exponential). */
 /* HadamardMlp.Apply (src/Needle/Blocks.cs:1067-1093) on `count` residual
  * rows [count][Dim] (device memory, updated in place) with layer `layer`'s
  * MLP factors and pre-norm scale and the model's two permutations; `scale`
  * as MlpBatch.Scale.  One block per row, the same kernel as the KernelTable
- * slot (inner sums in the scalar order; the condition softmax and the SiLU
- * through expf, tolerance).  A tensor shorter than the HadaRows x HadaCols
+ * slot (inner sums in the scalar order, MathF.Exp correctly rounded: bit for
+ * bit the scalar code).  A tensor shorter than the HadaRows x HadaCols
  * split needs is NDL_ERR_UNSUPPORTED. */
 NDL_API int ndl_mlp_apply(const ndl_model *m, int layer, float *residual, int count, float scale, void *stream);
 NDL_API size_t ndl_engram_workspace(const ndl_model *m, int count);
@@ -791,6 +793,29 @@ NDL_API int ndl_engram_apply(const ndl_model *m, int site, const int32_t *tokens
                              const int32_t *slot_length, const int32_t *slot_prev, int slots, const float *history_in,
                              float *history_out, const float *x, float *residual, void *workspace,
                              size_t workspace_bytes, void *stream);
+
+/* A batched decode engine over a loaded Needle-3 model (Model.Open + new
+ * BatchedEngine on a real archive; src/Needle/Model.cs:400-425,
+ * src/Needle/BatchEngine.cs:9-14).  ndl_forward_batch then runs
+ * EngineCore.ForwardBatch with RunLayerBatch (src/Needle/Engine.cs:
+ * 2303-2596) on the device in the reference's scalar tier, bit for bit:
+ * embedding GatherRow and scale, the hyper-connection prepare / phi matmuls /
+ * gates / Mix4 / Sinkhorn, Engram at its site layers, attention (CQ
+ * projections, 3-tap convs over each slot's two previous projections,
+ * ZeroCenteredRms and RoPE per head, an int8 K / V cache per slot, grouped
+ * heads with the sliding window on local layers, the gated output and
+ * PostNormAdd), the Kronecker MLP and CombineDiff4x4, then the head rows'
+ * logits over the vocabulary (PrepareHeadVectors and the tied embedding).
+ * A run of rows of one slot is equivalent to feeding them one at a time, and
+ * is computed that way.  Slot state (lengths, previous tokens, conv and
+ * Engram histories, K / V cache) is per slot on the device; ndl_slot_reset
+ * clears it.  Sampling, masks, top-k and ndl_batch_logits_row work as on
+ * the synthetic decoder.  Not available on this engine (NDL_ERR_UNSUPPORTED):
+ * mark / rewind, slot copies, prefixes, cross memory, the sparse head, the
+ * tensor views and the attention timer.  The model must stay loaded while
+ * the engine lives; capacity is at most 8192 and the model's head dims at
+ * most 64. */
+NDL_API int ndl_engine_create_model(const ndl_engine_config *engine, const ndl_model *model, ndl_engine **out);
 
 #ifdef __cplusplus
 }

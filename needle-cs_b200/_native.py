@@ -42,6 +42,7 @@ SIGNATURES = {
     "ndl_attention_paged_noalloc": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p, c_int,
                                             c_int, c_void_p, c_size_t, c_int, c_int, c_void_p, c_void_p, c_void_p]),
     "ndl_engine_create": (c_int, [c_void_p, c_void_p, ctypes.POINTER(c_void_p)]),
+    "ndl_engine_create_model": (c_int, [c_void_p, c_void_p, ctypes.POINTER(c_void_p)]),
     "ndl_engine_destroy": (c_int, [c_void_p]),
     "ndl_engine_stream": (c_int, [c_void_p, ctypes.POINTER(c_void_p)]),
     "ndl_engine_tensor": (c_int, [c_void_p, c_char_p, c_int, ctypes.POINTER(c_void_p), ctypes.POINTER(c_size_t)]),

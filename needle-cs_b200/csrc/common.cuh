@@ -147,6 +147,45 @@ __device__ __forceinline__ float exp_simd(float x) {
 __device__ __forceinline__ float sigmoid_simd(float x) {
     return __fdiv_rn(1.0f, __fadd_rn(1.0f, exp_simd(__fsub_rn(0.0f, x))));
 }
+
+// MathF.Exp where the reference's scalar tier calls it (Softmax, Sigmoid,
+// Sinkhorn4x4, the Needle-3 gates, MLP and Engram): the float exponential
+// rounded to nearest, computed in double precision from the mathematics
+// (Cody and Waite's reduction with fdlibm's two-part ln 2, then the Taylor
+// series to degree 13), which equals the correctly rounded exp except within
+// about 1e-15 of a rounding midpoint.  Every double step is an explicit
+// IEEE operation, so the CPU oracle, which evaluates the same steps, returns
+// the same bits.
+__device__ __forceinline__ float exp_rn(float x) {
+    if (x != x) return x;
+    if (x > 89.0f) return __int_as_float(0x7f800000);
+    if (x < -104.0f) return 0.0f;
+    const double xd = (double)x;
+    const double k = rint(__dmul_rn(xd, 1.4426950408889634));
+    const double r =
+        __dsub_rn(__dsub_rn(xd, __dmul_rn(k, 6.93147180369123816490e-01)), __dmul_rn(k, 1.90821492927058770002e-10));
+    double p = 1.6059043836821614599e-10;      // 1/13!
+    p = __fma_rn(p, r, 2.0876756987868098979e-09);  // 1/12!
+    p = __fma_rn(p, r, 2.5052108385441718775e-08);  // 1/11!
+    p = __fma_rn(p, r, 2.7557319223985890653e-07);  // 1/10!
+    p = __fma_rn(p, r, 2.7557319223985890653e-06);  // 1/9!
+    p = __fma_rn(p, r, 2.4801587301587301587e-05);  // 1/8!
+    p = __fma_rn(p, r, 1.9841269841269841270e-04);  // 1/7!
+    p = __fma_rn(p, r, 1.3888888888888888889e-03);  // 1/6!
+    p = __fma_rn(p, r, 8.3333333333333333333e-03);  // 1/5!
+    p = __fma_rn(p, r, 4.1666666666666666667e-02);  // 1/4!
+    p = __fma_rn(p, r, 1.6666666666666666667e-01);  // 1/3!
+    p = __fma_rn(p, r, 0.5);
+    p = __fma_rn(p, r, 1.0);
+    p = __fma_rn(p, r, 1.0);
+    // times 2^k (|k| <= 151: exact in double), one rounding to float
+    const double two_k = __longlong_as_double((long long)((int)k + 1023) << 52);
+    return __double2float_rn(__dmul_rn(p, two_k));
+}
+// Ops.Sigmoid's scalar form (src/Needle/Ops.cs:88): 1 / (1 + MathF.Exp(-x)).
+__device__ __forceinline__ float sigmoid_rn(float x) {
+    return __fdiv_rn(1.0f, __fadd_rn(1.0f, exp_rn(-x)));
+}
 #endif
 
 // IEEE round-to-nearest-even float -> binary16 (integer-only).

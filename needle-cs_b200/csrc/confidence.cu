@@ -10,7 +10,8 @@
 // gained, with a row bias) and projects the pooled queries.  State lives in
 // caller-owned device arrays; the reference's snapshot / restore after a
 // rewind is the optional snapshot arrays and per-slot pending flags.  Sums run
-// in the scalar code's order; exp makes the results tolerance-equal.
+// in the scalar code's order and MathF.Exp is the correctly rounded
+// exponential (exp_rn), so the results equal the scalar code's bit for bit.
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -71,13 +72,13 @@ __global__ void __launch_bounds__(256) conf_pool_kernel(ConfPoolArgs a) {
             const float score = __fmul_rn(dot, inverse_root);
             const float mx = a.pool_max[at];
             if (score > mx) {
-                const float rescale = expf(__fsub_rn(mx, score));
+                const float rescale = exp_rn(__fsub_rn(mx, score));
                 a.pool_sum[at] = __fadd_rn(__fmul_rn(a.pool_sum[at], rescale), 1.0f);
                 a.pool_max[at] = score;
                 factor = rescale;
                 grow = 1;
             } else {
-                const float weight = expf(__fsub_rn(score, mx));
+                const float weight = exp_rn(__fsub_rn(score, mx));
                 a.pool_sum[at] = __fadd_rn(a.pool_sum[at], weight);
                 factor = weight;
                 grow = 0;
@@ -143,7 +144,7 @@ __global__ void __launch_bounds__(256) conf_logit_kernel(ConfLogitArgs a) {
             float peak = -INFINITY, total = 0.0f;
             for (int i = 0; i < rows; i++) peak = fmaxf(peak, w[i]);
             for (int i = 0; i < rows; i++) {
-                w[i] = expf(__fsub_rn(w[i], peak));
+                w[i] = exp_rn(__fsub_rn(w[i], peak));
                 total = __fadd_rn(total, w[i]);
             }
             for (int i = 0; i < rows; i++) w[i] = __fdiv_rn(w[i], total);

@@ -19,6 +19,7 @@
 
 #include "common.cuh"
 #include "kernels.cuh"
+#include "needle3.cuh"
 #include "kv.cuh"
 
 namespace ndl {
@@ -69,6 +70,7 @@ struct DeviceLayer {
 struct ndl_engine {
     ndl_engine_config ec{};
     ndl_decoder_config dc{};
+    ndl::N3State *n3 = nullptr;  // set: a Needle-3 engine over a loaded model (ndl_engine_create_model)
     cudaStream_t stream = nullptr;
     bool own_stream = false;
     std::vector<void *> allocations;
@@ -289,6 +291,8 @@ int build_weights(ndl_engine *e) {
     return NDL_OK;
 }
 
+int build_sampling_buffers(ndl_engine *e);
+
 int build_buffers(ndl_engine *e) {
     const ndl_decoder_config &c = e->dc;
     const int R = e->ec.max_rows, Hd = e->ec.max_heads, d = c.dim, F = c.ffn;
@@ -309,17 +313,24 @@ int build_buffers(ndl_engine *e) {
         if (c.cross) TRY(dalloc(e, &e->cross_work, records));
         TRY(dalloc(e, &e->n_work, 8));  // int[4] per list (self, cross)
     }
-    TRY(dalloc(e, &e->d_status, 1));
-    NDL_CUDA(cudaMemsetAsync(e->d_status, 0, sizeof(int), e->stream));
     // metadata: tokens, slots, positions, order, memory slot, memory position
     // (R each) + head rows (Hd) + updates (3 per row + slack)
     e->meta_ints = (size_t)6 * R + Hd + 3 * (size_t)R + 64;
     TRY(dalloc(e, &e->d_meta, e->meta_ints));
     NDL_CUDA(cudaMallocHost(&e->h_meta, e->meta_ints * sizeof(int32_t)));
+    return build_sampling_buffers(e);
+}
+
+// The logits, status word and sampling buffers every engine kind has.
+int build_sampling_buffers(ndl_engine *e) {
+    const int Hd = e->ec.max_heads, V = e->dc.vocab;
+    if (!e->logits) TRY(dalloc(e, &e->logits, (size_t)Hd * V));
+    TRY(dalloc(e, &e->d_status, 1));
+    NDL_CUDA(cudaMemsetAsync(e->d_status, 0, sizeof(int), e->stream));
     TRY(dalloc(e, &e->d_ids, (size_t)Hd * 8));
     TRY(dalloc(e, &e->d_probs, (size_t)Hd * 8));
     TRY(dalloc(e, &e->d_logp, (size_t)Hd * 8));
-    int words = (c.vocab + 31) / 32;
+    int words = (V + 31) / 32;
     TRY(dalloc(e, &e->d_masks, (size_t)Hd * words));
     NDL_CUDA(cudaMallocHost(&e->h_out, (size_t)Hd * 8 * 12 + (size_t)Hd * words * 4 + 64));
     NDL_CUDA(cudaStreamSynchronize(e->stream));
@@ -662,9 +673,55 @@ NDL_API int ndl_engine_create(const ndl_engine_config *ec, const ndl_decoder_con
     return NDL_OK;
 }
 
+// A Needle-3 engine over a loaded .cact model (ndl_model_load with a device):
+// its steps are the model's RunLayerBatch chain (needle3.cu); sampling, masks
+// and logits work as for the synthetic decoder.
+NDL_API int ndl_engine_create_model(const ndl_engine_config *ec, const ndl_model *m, ndl_engine **out) {
+    NDL_REQUIRE(ec && m && out, "null argument");
+    *out = nullptr;
+    ndl_model_info info;
+    int st = ndl_model_get_info(m, &info);
+    if (st != NDL_OK) return st;
+    NDL_REQUIRE(info.device >= 0, "the model is not on a device");
+    NDL_REQUIRE(ec->device == info.device, "engine device %d, model device %d", ec->device, info.device);
+    NDL_REQUIRE(ec->slots >= 1 && ec->capacity >= 1, "slots and capacity must be positive");
+    NDL_REQUIRE(ec->max_rows >= 1 && ec->max_heads >= 1 && ec->max_heads <= ec->max_rows, "bad row limits");
+    NDL_CUDA(cudaSetDevice(ec->device));
+    ndl_engine *e = new ndl_engine();
+    e->ec = *ec;
+    e->dc = ndl_decoder_config{};
+    e->dc.layers = info.layers;
+    e->dc.dim = info.dim;
+    e->dc.heads = info.heads;
+    e->dc.head_dim = info.qk_dim;
+    e->dc.vocab = info.vocab;
+    cudaError_t err = cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking);
+    if (err != cudaSuccess) {
+        delete e;
+        return set_error(NDL_ERR_CUDA, "stream: %s", cudaGetErrorString(err));
+    }
+    e->own_stream = true;
+    e->use_graphs = false;
+    st = ndl::n3_create(m, ec->slots, ec->capacity, ec->max_rows, ec->max_heads, e->stream, &e->n3);
+    if (st == NDL_OK) {
+        e->dc.vocab = ndl::n3_vocab(e->n3);
+        st = build_sampling_buffers(e);
+    }
+    if (st != NDL_OK) {
+        ndl_engine_destroy(e);
+        return st;
+    }
+    e->slot_len.assign(ec->slots, 0);
+    e->slot_mark.assign(ec->slots, 0);
+    e->cross_slot.assign(ec->slots, -1);
+    *out = e;
+    return NDL_OK;
+}
+
 NDL_API int ndl_engine_destroy(ndl_engine *e) {
     if (!e) return NDL_OK;
     if (e->stream) cudaStreamSynchronize(e->stream);
+    ndl::n3_destroy(e->n3);
     for (auto &g : e->graphs) cudaGraphExecDestroy(g.exec);
     for (cudaEvent_t ev : e->event_pool) cudaEventDestroy(ev);
     for (void *p : e->allocations) cudaFree(p);
@@ -685,6 +742,7 @@ NDL_API int ndl_engine_stream(ndl_engine *e, void **stream) {
 }
 
 NDL_API int ndl_engine_tensor(ndl_engine *e, const char *name, int layer, void **ptr, size_t *bytes) {
+    if (e && e->n3) return set_error(NDL_ERR_UNSUPPORTED, "%s: not available on a Needle-3 engine", "ndl_engine_tensor");
     NDL_REQUIRE(e && name && ptr && bytes, "null argument");
     const ndl_decoder_config &c = e->dc;
     const size_t d = c.dim, F = c.ffn, V = c.vocab, G = d / 32, GF = F / 32;
@@ -726,6 +784,7 @@ NDL_API int ndl_engine_tensor(ndl_engine *e, const char *name, int layer, void *
 }
 
 NDL_API int ndl_engine_read_tensor(ndl_engine *e, const char *name, int layer, void *host, size_t bytes) {
+    if (e && e->n3) return set_error(NDL_ERR_UNSUPPORTED, "%s: not available on a Needle-3 engine", "ndl_engine_read_tensor");
     void *ptr = nullptr;
     size_t have = 0;
     TRY(ndl_engine_tensor(e, name, layer, &ptr, &have));
@@ -736,6 +795,7 @@ NDL_API int ndl_engine_read_tensor(ndl_engine *e, const char *name, int layer, v
 }
 
 NDL_API int ndl_engine_page_bytes(ndl_engine *e, size_t *bytes) {
+    if (e && e->n3) return set_error(NDL_ERR_UNSUPPORTED, "%s: not available on a Needle-3 engine", "ndl_engine_page_bytes");
     NDL_REQUIRE(e && bytes, "null argument");
     *bytes = e->page_bytes;
     return NDL_OK;
@@ -749,6 +809,7 @@ NDL_API int ndl_slot_length(ndl_engine *e, int slot, int *length) {
 }
 
 NDL_API int ndl_slot_page(ndl_engine *e, int slot, int index, int *page) {
+    if (e && e->n3) return set_error(NDL_ERR_UNSUPPORTED, "%s: not available on a Needle-3 engine", "ndl_slot_page");
     TRY(check_slot(e, slot));
     NDL_REQUIRE(page && index >= 0 && index < e->max_pages, "bad page index");
     *page = e->page_table[(size_t)slot * e->max_pages + index];
@@ -758,6 +819,12 @@ NDL_API int ndl_slot_page(ndl_engine *e, int slot, int index, int *page) {
 // EngineCore.ResetSlot (src/Needle/Engine.cs:2267-2271): empty the slot.
 NDL_API int ndl_slot_reset(ndl_engine *e, int slot) {
     TRY(check_slot(e, slot));
+    if (e->n3) {
+        TRY(ndl::n3_reset_slot(e->n3, slot, e->stream));
+        e->slot_len[slot] = 0;
+        e->slot_mark[slot] = 0;
+        return NDL_OK;
+    }
     std::vector<int32_t> updates;
     free_slot_pages(e, slot, 0, &updates);
     e->slot_len[slot] = 0;
@@ -767,6 +834,7 @@ NDL_API int ndl_slot_reset(ndl_engine *e, int slot) {
 
 // EngineCore.MarkSlot (src/Needle/Engine.cs:2273-2277): remember the length.
 NDL_API int ndl_slot_mark(ndl_engine *e, int slot) {
+    if (e && e->n3) return set_error(NDL_ERR_UNSUPPORTED, "%s: not available on a Needle-3 engine", "ndl_slot_mark");
     TRY(check_slot(e, slot));
     e->slot_mark[slot] = e->slot_len[slot];
     return NDL_OK;
@@ -775,6 +843,7 @@ NDL_API int ndl_slot_mark(ndl_engine *e, int slot) {
 // EngineCore.RewindSlot (src/Needle/Engine.cs:2279-2283): back to the mark;
 // pages wholly past the mark are returned to the pool.
 NDL_API int ndl_slot_rewind(ndl_engine *e, int slot) {
+    if (e && e->n3) return set_error(NDL_ERR_UNSUPPORTED, "%s: not available on a Needle-3 engine", "ndl_slot_rewind");
     TRY(check_slot(e, slot));
     std::vector<int32_t> updates;
     int keep = (e->slot_mark[slot] + kPagePositions - 1) / kPagePositions;
@@ -786,6 +855,7 @@ NDL_API int ndl_slot_rewind(ndl_engine *e, int slot) {
 // Fills positions [len, len+count) of a slot with the synthetic prefix K/V
 // (fp16 N(0,1) quantized on load) and advances its length.
 NDL_API int ndl_slot_fill_synthetic(ndl_engine *e, int slot, int count, uint64_t seed, uint64_t session) {
+    if (e && e->n3) return set_error(NDL_ERR_UNSUPPORTED, "%s: not available on a Needle-3 engine", "ndl_slot_fill_synthetic");
     TRY(check_slot(e, slot));
     NDL_REQUIRE(count >= 0, "count < 0");
     int first = e->slot_len[slot];
@@ -866,6 +936,7 @@ int check_memory_slot(ndl_engine *e, int slot, int frames) {
 }  // namespace
 
 NDL_API int ndl_slot_set_memory(ndl_engine *e, int slot, const uint16_t *memory, int frames) {
+    if (e && e->n3) return set_error(NDL_ERR_UNSUPPORTED, "%s: not available on a Needle-3 engine", "ndl_slot_set_memory");
     NDL_REQUIRE(e && memory, "null argument");
     TRY(check_memory_slot(e, slot, frames));
     const size_t bytes = (size_t)frames * e->dc.dim * 2;
@@ -883,6 +954,7 @@ NDL_API int ndl_slot_set_memory(ndl_engine *e, int slot, const uint16_t *memory,
 }
 
 NDL_API int ndl_slot_fill_memory_synthetic(ndl_engine *e, int slot, int frames, uint64_t seed, uint64_t utterance) {
+    if (e && e->n3) return set_error(NDL_ERR_UNSUPPORTED, "%s: not available on a Needle-3 engine", "ndl_slot_fill_memory_synthetic");
     NDL_REQUIRE(e, "null engine");
     TRY(check_memory_slot(e, slot, frames));
     const size_t count = (size_t)frames * e->dc.dim;
@@ -899,6 +971,7 @@ NDL_API int ndl_slot_fill_memory_synthetic(ndl_engine *e, int slot, int frames, 
 }
 
 NDL_API int ndl_slot_attach_memory(ndl_engine *e, int slot, int memory_slot) {
+    if (e && e->n3) return set_error(NDL_ERR_UNSUPPORTED, "%s: not available on a Needle-3 engine", "ndl_slot_attach_memory");
     NDL_REQUIRE(e, "null engine");
     TRY(check_slot(e, slot));
     NDL_REQUIRE(e->dc.cross, "the decoder has no cross-attention blocks");
@@ -909,6 +982,7 @@ NDL_API int ndl_slot_attach_memory(ndl_engine *e, int slot, int memory_slot) {
 }
 
 NDL_API int ndl_slot_copy(ndl_engine *e, int dst, int src) {
+    if (e && e->n3) return set_error(NDL_ERR_UNSUPPORTED, "%s: not available on a Needle-3 engine", "ndl_slot_copy");
     NDL_REQUIRE(e, "null engine");
     TRY(check_slot(e, dst));
     TRY(check_slot(e, src));
@@ -936,6 +1010,14 @@ NDL_API int ndl_forward_batch(ndl_engine *e, const int *tokens, const int *row_s
     NDL_REQUIRE(rows >= 1 && rows <= e->ec.max_rows, "rows %d outside 1..%d", rows, e->ec.max_rows);
     NDL_REQUIRE(heads >= 0 && heads <= e->ec.max_heads && heads <= rows, "heads %d out of range", heads);
     NDL_REQUIRE(tokens && row_slots && (heads == 0 || head_rows), "null argument");
+    if (e->n3) {
+        int st = ndl::n3_forward(e->n3, e->stream, tokens, row_slots, rows, head_rows, heads, e->logits);
+        if (st != NDL_OK) return st;
+        for (int r = 0; r < rows; r++) e->slot_len[row_slots[r]]++;
+        e->last_rows = rows;
+        e->last_heads = heads;
+        return check_status(e);
+    }
     const ndl_decoder_config &c = e->dc;
     // positions, capacity check, page allocation (host)
     int32_t *m = e->h_meta;
@@ -1096,6 +1178,7 @@ NDL_API int ndl_engine_get_info(ndl_engine *e, ndl_engine_info *info) {
 // aid for the attention roofline: the launches rewrite the step's scratch
 // outputs (the query is the last layer's), nothing a later step reads.
 NDL_API int ndl_engine_time_attention(ndl_engine *e, int layer, int reps, float *ms) {
+    if (e && e->n3) return set_error(NDL_ERR_UNSUPPORTED, "%s: not available on a Needle-3 engine", "ndl_engine_time_attention");
     NDL_REQUIRE(e && ms, "null argument");
     NDL_REQUIRE(e->last_rows > 0, "no step has run");
     NDL_REQUIRE(layer >= 0 && layer < e->dc.layers && reps >= 1, "layer %d / reps %d out of range", layer, reps);
@@ -1124,6 +1207,7 @@ NDL_API int ndl_engine_time_attention(ndl_engine *e, int layer, int reps, float 
 
 // Pool pages not held by any slot.
 NDL_API int ndl_engine_free_pages(ndl_engine *e, int *free_pages) {
+    if (e && e->n3) return set_error(NDL_ERR_UNSUPPORTED, "%s: not available on a Needle-3 engine", "ndl_engine_free_pages");
     NDL_REQUIRE(e && free_pages, "null argument");
     *free_pages = (int)e->free_pages.size();
     return NDL_OK;
@@ -1132,6 +1216,7 @@ NDL_API int ndl_engine_free_pages(ndl_engine *e, int *free_pages) {
 // Engine.PrimedPrefixBytes (src/Needle/Engine.cs:398-400): bytes of the blob
 // of the slot's marked prefix (its length at ndl_slot_mark).
 NDL_API int ndl_slot_prefix_bytes(ndl_engine *e, int slot, size_t *bytes) {
+    if (e && e->n3) return set_error(NDL_ERR_UNSUPPORTED, "%s: not available on a Needle-3 engine", "ndl_slot_prefix_bytes");
     NDL_REQUIRE(e && bytes, "null argument");
     TRY(check_slot(e, slot));
     *bytes = prefix_blob_bytes(e->dc.layers, e->dc.heads, e->slot_mark[slot]);
@@ -1141,6 +1226,7 @@ NDL_API int ndl_slot_prefix_bytes(ndl_engine *e, int slot, size_t *bytes) {
 // Engine.ExportPrimedPrefix (src/Needle/Engine.cs:402-427): the slot's
 // marked prefix as a blob (layout in prefix.cu).
 NDL_API int ndl_slot_export_prefix(ndl_engine *e, int slot, void *blob, size_t bytes) {
+    if (e && e->n3) return set_error(NDL_ERR_UNSUPPORTED, "%s: not available on a Needle-3 engine", "ndl_slot_export_prefix");
     NDL_REQUIRE(e && blob, "null argument");
     TRY(check_slot(e, slot));
     const int len = e->slot_mark[slot];
@@ -1161,6 +1247,7 @@ NDL_API int ndl_slot_export_prefix(ndl_engine *e, int slot, void *blob, size_t b
 // Engine.ImportPrimedPrefix (src/Needle/Engine.cs:429-464): the slot's cache
 // becomes the blob's prefix; its length and mark are the blob's length.
 NDL_API int ndl_slot_import_prefix(ndl_engine *e, int slot, const void *blob, size_t bytes) {
+    if (e && e->n3) return set_error(NDL_ERR_UNSUPPORTED, "%s: not available on a Needle-3 engine", "ndl_slot_import_prefix");
     NDL_REQUIRE(e && blob, "null argument");
     TRY(check_slot(e, slot));
     NDL_REQUIRE(bytes >= 4, "primed prefix is truncated");
@@ -1189,6 +1276,7 @@ NDL_API int ndl_slot_import_prefix(ndl_engine *e, int slot, const void *blob, si
 // copied.  A later write into a shared page copies it first (copy on write),
 // so neither slot sees the other's new positions.
 NDL_API int ndl_slot_share_prefix(ndl_engine *e, int dst, int src) {
+    if (e && e->n3) return set_error(NDL_ERR_UNSUPPORTED, "%s: not available on a Needle-3 engine", "ndl_slot_share_prefix");
     NDL_REQUIRE(e, "null engine");
     TRY(check_slot(e, dst));
     TRY(check_slot(e, src));
@@ -1271,6 +1359,7 @@ static int sparse_reserve(ndl_engine *e, size_t total) {
 // row-dot launch, one argmax launch.
 NDL_API int ndl_logits_sparse(ndl_engine *e, int n, const int *rows, const int *offsets, const int *ids,
                               float *values, int *picks, float *probs) {
+    if (e && e->n3) return set_error(NDL_ERR_UNSUPPORTED, "%s: not available on a Needle-3 engine", "ndl_logits_sparse");
     NDL_REQUIRE(e, "engine is NULL");
     const int Hd = e->ec.max_heads, V = e->dc.vocab, d = e->dc.dim;
     NDL_REQUIRE(n >= 0 && n <= Hd, "%d requests outside 0..%d", n, Hd);

@@ -123,7 +123,7 @@ __global__ void __launch_bounds__(256) engram_gate_kernel(const float *__restric
         float dot = 0.0f;
         for (int i = 0; i < dim; i++) dot = __fadd_rn(dot, __fmul_rn(__fmul_rn(xt[i], ia), __fmul_rn(kt[i], ib)));
         const float z = __fmul_rn(dot, __fdiv_rn(1.0f, __fsqrt_rn((float)dim)));
-        alpha = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-z)));
+        alpha = sigmoid_rn(z);
     }
     alpha = __shfl_sync(0xffffffffu, alpha, 0);
     float *rt = residual + (size_t)t * dim;

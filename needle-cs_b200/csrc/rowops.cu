@@ -74,7 +74,7 @@ __global__ void __launch_bounds__(128) sinkhorn4x4_kernel(const float *__restric
     for (int row = 0; row < 4; row++) {
         const float peak = fmaxf(fmaxf(lg[row * 4], lg[row * 4 + 1]), fmaxf(lg[row * 4 + 2], lg[row * 4 + 3]));
 #pragma unroll
-        for (int c = 0; c < 4; c++) r[row * 4 + c] = expf(__fsub_rn(lg[row * 4 + c], peak));
+        for (int c = 0; c < 4; c++) r[row * 4 + c] = exp_rn(__fsub_rn(lg[row * 4 + c], peak));
     }
     for (int it = 0; it < 20; it++) {
 #pragma unroll
@@ -140,7 +140,7 @@ __global__ void __launch_bounds__(256) fake_a8_kernel(const float *__restrict__ 
         float v;
         if (MODE == 0) v = __fmul_rn(xr[i], inverse);
         else if (MODE == 1) v = __fmul_rn(__fmul_rn(__fadd_rn(1.0f, aux[i]), xr[i]), inverse);
-        else v = __fmul_rn(xr[i], __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-aux[(size_t)row * n + i]))));
+        else v = __fmul_rn(xr[i], sigmoid_rn(aux[(size_t)row * n + i]));
         dr[i] = v;
         peak = fmaxf(peak, fabsf(v));
     }
@@ -193,7 +193,7 @@ __global__ void __launch_bounds__(32) slot_vec_kernel(float *__restrict__ x, con
         for (int i = lane; i < n; i += 32) peak = fmaxf(peak, x[i]);
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) peak = fmaxf(peak, __shfl_xor_sync(0xffffffffu, peak, o));
-        for (int i = lane; i < n; i += 32) x[i] = expf(__fsub_rn(x[i], peak));
+        for (int i = lane; i < n; i += 32) x[i] = exp_rn(__fsub_rn(x[i], peak));
         __syncwarp();
         float total = 0.0f;
         if (lane == 0)
@@ -290,7 +290,7 @@ __global__ void __launch_bounds__(192) slot_attention_tile_kernel(KtTileArgs a) 
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) peak = fmaxf(peak, __shfl_xor_sync(0xffffffffu, peak, o));
-    for (int s = lane; s < a.count; s += 32) sc[s] = expf(__fsub_rn(sc[s], peak));
+    for (int s = lane; s < a.count; s += 32) sc[s] = exp_rn(__fsub_rn(sc[s], peak));
     __syncwarp();
     float total = 0.0f;
     if (lane == 0)
@@ -332,7 +332,7 @@ __global__ void __launch_bounds__(192) slot_merge_partials_kernel(const float *_
         if (count == 2) {
             const float p0 = p[kPeak + h], p1 = p[kStride + kPeak + h];
             const float pk = fmaxf(p0, p1);
-            const float w0 = expf(__fsub_rn(p0, pk)), w1 = expf(__fsub_rn(p1, pk));
+            const float w0 = exp_rn(__fsub_rn(p0, pk)), w1 = exp_rn(__fsub_rn(p1, pk));
             float tot = __fadd_rn(0.0f, __fmul_rn(w0, p[kPeak + 8 + h]));
             tot = __fadd_rn(tot, __fmul_rn(w1, p[kStride + kPeak + 8 + h]));
             const float inv = __fdiv_rn(1.0f, tot);
@@ -342,7 +342,7 @@ __global__ void __launch_bounds__(192) slot_merge_partials_kernel(const float *_
             for (int c = 0; c < count; c++) peak = fmaxf(peak, p[c * kStride + kPeak + h]);
             float total = 0.0f, sum = 0.0f;
             for (int c = 0; c < count; c++) {
-                const float w = expf(__fsub_rn(p[c * kStride + kPeak + h], peak));
+                const float w = exp_rn(__fsub_rn(p[c * kStride + kPeak + h], peak));
                 total = __fadd_rn(total, __fmul_rn(w, p[c * kStride + kPeak + 8 + h]));
                 sum = __fadd_rn(sum, __fmul_rn(w, p[c * kStride + h * 64 + d]));
             }
@@ -424,7 +424,7 @@ __global__ void __launch_bounds__(256) slot_hadamard_mlp_kernel(KtMlpArgs a) {
         float peak = -INFINITY, total = 0.0f;
         for (int j = 0; j < 8; j++) peak = fmaxf(peak, weights[j]);
         for (int j = 0; j < 8; j++) {
-            weights[j] = expf(__fsub_rn(weights[j], peak));
+            weights[j] = exp_rn(__fsub_rn(weights[j], peak));
             total = __fadd_rn(total, weights[j]);
         }
         for (int j = 0; j < 8; j++) weights[j] = __fdiv_rn(weights[j], total);
@@ -437,7 +437,7 @@ __global__ void __launch_bounds__(256) slot_hadamard_mlp_kernel(KtMlpArgs a) {
         float condition = 1.0f;
         for (int j = 0; j < 8; j++) condition = __fadd_rn(condition, __fmul_rn(weights[j], a.w[12][j * width + n]));
         const float v = __fadd_rn(__fmul_rn(__fmul_rn(d2[n], condition), back[a.perm_a[n]]), b2[n]);
-        front[n] = __fmul_rn(v, __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-v))));
+        front[n] = __fmul_rn(v, sigmoid_rn(v));
     }
     __syncthreads();
     mlp_kron(front, rows, a.w[7], a.w[8], rows, cols, rows, tmp, back);

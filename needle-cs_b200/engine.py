@@ -60,6 +60,27 @@ class BatchedEngine:
         self.max_heads = max_heads
         self._last_heads = 0
 
+    @classmethod
+    def from_model(cls, model, slots=8, context_length=512, chunk_size=64, max_heads=None):
+        """A batched engine over a loaded Needle-3 archive (needle_cs_b200.model.Model
+        on a device): ndl_engine_create_model.  Forwards run the model's
+        RunLayerBatch chain; the model must outlive the engine."""
+        self = cls.__new__(cls)
+        self.model = model
+        self.chunk = chunk_size
+        max_heads = max_heads or chunk_size
+        info = model.info
+        cfg = EngineConfig(info["device"], slots, context_length, 0, chunk_size, max_heads)
+        handle = ctypes.c_void_p()
+        call("ndl_engine_create_model", ctypes.byref(cfg), model._h, ctypes.byref(handle))
+        self._h = handle
+        self.slots = slots
+        self.capacity = context_length
+        self.vocab_size = info["vocab"]
+        self.max_heads = max_heads
+        self._last_heads = 0
+        return self
+
     # -- lifetime --
     def close(self):
         if self._h:

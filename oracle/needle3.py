@@ -1,0 +1,286 @@
+"""CPU restatement of the Needle-3 batched decode step (EngineCore.ForwardBatch
+with RunLayerBatch, src/Needle/Engine.cs:2303-2596), the reference's scalar
+tier throughout (Simd.Enabled false: MathF.Exp, no fused multiply-adds).
+
+TEST INFRASTRUCTURE ONLY.  The checker for the device chain in the library's
+Needle-3 engine; never imported by the library.  Every operation is a call of
+the C oracle's restatement of the reference routine (each cites its
+file:line there); this file only chains them in RunLayerBatch's order:
+
+  ForwardBatch (Engine.cs:2303-2350)
+    embedding: GatherRow, x += x * (sqrt(dim) - 1) (AddScaled, Scalar.cs:275),
+    copied to the 4 streams; Engram rows hashed from the tokens
+    per layer, RunLayerBatch (:2352-2404):
+      PrepareRmsFakeA8 of the 4-stream row at 4 bits; phi pre / post / res
+      CQ matmuls on the layer's row slices; hpre = sigmoid(a_pre * pre +
+      b_pre + (lane ? 4 : -4)), post_gate = 2 sigmoid(a_post * post + b_post +
+      (lane ? 0 : -4)); u = Mix4(s, hpre); mix = Sinkhorn4x4(a_res * res +
+      b_res); residual = u
+      Engram at a site layer (ApplyEngramBatch, :2405-2469)
+      RunAttentionBatch (:2480-2596): PrepareCenteredRmsFakeA8(residual,
+      norm_in) at 2 bits; Q, K, V, gate CQ matmuls; 3-tap convs over the
+      slot's two previous projections (ChainTriple / Taps3); per head
+      ZeroCenteredRms (q_norm, k_norm) and RoPE at the row's position;
+      QuantizeInt8 of q per head and of k, v per kv head into the slot's
+      cache; AttentionHead over [first, position] (sliding window on local
+      layers); PrepareGateFakeA8(out, gate) at 2 bits; out CQ matmul;
+      PostNormAdd(residual, ., post_norm, sigmoid(attn_gate))
+      RunMlp: HadamardMlp.Apply (scale 1)
+      CombineDiff4x4(s, mix, residual, u, post_gate) -> next streams
+    per slot: previous tokens and length advance
+    heads: PrepareHeadVectors (Mix4 of the streams by 1/4, ZeroCenteredRms
+    with final_norm, FakeA8, Prepare at 4 bits), then the embedding CQ matmul
+    over the vocabulary.
+
+Rows of one forward are distinct slots (the library's engine feeds a run of
+one slot as consecutive forwards, which the reference's run semantics equal:
+ChainTriple, the Engram window and the causal attention of a run see exactly
+what sequential single-row forwards see).
+"""
+import ctypes
+
+import numpy as np
+
+from . import oracle as O
+
+LANES = 4
+CONV_TAPS = 3
+ENGRAM_HISTORY = 9
+
+
+def _f(a):
+    return np.ascontiguousarray(a, np.float32)
+
+
+class Needle3Oracle:
+    """`dense(role, i)` -> float32 array, `cq(role, i)` -> (codes [rows][cols*bits/8]
+    uint8, norms [rows][cols/128] uint16, rows, cols, bits), `perm(role)` ->
+    int32 array, `info` the geometry dict of ndl_model_get_info, `levels` the
+    codebook's 28 levels."""
+
+    def __init__(self, info, levels, dense, cq, perm, slots, capacity):
+        self.g = info
+        self.dense, self.cq, self.perm = dense, cq, perm
+        self.book2 = O.codebook(np.asarray(levels[0:4], np.float32), 4)
+        self.book4 = O.codebook(np.asarray(levels[12:28], np.float32), 16)
+        self.levels4 = np.asarray(levels[12:28], np.float32)
+        g = info
+        self.dim = g["dim"]
+        self.qw, self.kw, self.vw = g["heads"] * g["qk_dim"], g["kv_heads"] * g["qk_dim"], g["kv_heads"] * g["v_dim"]
+        self.ow = g["heads"] * g["v_dim"]
+        self.slots, self.capacity = slots, capacity
+        self.cos, self.sin = O.rope_tables(g["rope_theta"], g["qk_dim"], capacity)
+        self.reset_all()
+
+    # -- state (EngineCore slot views) --
+    def reset_all(self):
+        g, L = self.g, self.g["layers"]
+        S, C = self.slots, self.capacity
+        self.length = np.zeros(S, np.int32)
+        self.prev = np.zeros((S, 2), np.int32)
+        self.qhist = np.zeros((S, L, CONV_TAPS - 1, self.qw), np.float32)
+        self.khist = np.zeros((S, L, CONV_TAPS - 1, self.kw), np.float32)
+        self.vhist = np.zeros((S, L, CONV_TAPS - 1, self.vw), np.float32)
+        self.keys = np.zeros((S, L, C, self.kw), np.int8)
+        self.kscale = np.zeros((S, L, C, g["kv_heads"]), np.float32)
+        self.values = np.zeros((S, L, C, self.vw), np.int8)
+        self.vscale = np.zeros((S, L, C, g["kv_heads"]), np.float32)
+        self.ehist = np.zeros((S, max(g["site_count"], 1), ENGRAM_HISTORY, self.dim), np.float32)
+
+    def reset_slot(self, s):
+        for a in (self.qhist, self.khist, self.vhist, self.keys, self.kscale, self.values, self.vscale, self.ehist,
+                  self.prev):
+            a[s] = 0
+        self.length[s] = 0
+
+    # -- pieces --
+    def _matmul(self, role, index, act, rows=None):
+        codes, norms, nrows, cols, bits = self.cq(role, index)
+        vals, sc, off, _ = act
+        book = self.book2 if bits == 2 else self.book4
+        r0, r1 = (0, nrows) if rows is None else rows
+        y = np.zeros((vals.shape[0], nrows), np.float32)
+        O.matmul_rows_cq(codes, norms, book, bits, vals, sc, off, r0, r1, y)
+        return y[:, r0:r1].copy()
+
+    def _site(self, layer):
+        sites = list(self.g["sites"][:self.g["site_count"]])
+        return sites.index(layer) if layer in sites else -1
+
+    def _engram(self, site, tokens, slots, u, residual):
+        g, lib = self.g, O.lib()
+        count, dim, tables = len(slots), self.dim, g["engram_tables"]
+        orders = np.array(g["orders"][:g["order_count"]], np.int32)
+        heads = tables // orders.size
+        rows = np.zeros((count, tables), np.int32)
+        tk, rs = np.asarray(tokens, np.int32), np.asarray(slots, np.int32)
+        lib.ndo_engram_hash(tk.ctypes.data, rs.ctypes.data, count, self.length.ctypes.data, self.prev.ctypes.data,
+                            orders.ctypes.data, orders.size, heads, g["engram_slots"], rows.ctypes.data)
+        codes, norms, _, cols, bits = self.cq("site.tables", site)
+        e = np.zeros((count, dim), np.float32)
+        for t in range(count):
+            for table in range(tables):
+                if rows[t, table] >= 0:
+                    e[t, table * cols:(table + 1) * cols] = O.gather_row_cq(codes, norms, self.levels4, bits,
+                                                                            int(rows[t, table]))
+            lib.ndo_fake_a8(e[t].ctypes.data, dim)
+        act = O.prepare_cq(e, 2)
+        key, value = self._matmul("site.key", site, act), self._matmul("site.value", site, act)
+        taps = _f(self.dense("site.taps", site)[:4 * dim])
+        conv = np.zeros((count, dim), np.float32)
+        hist_all = np.ascontiguousarray(self.ehist[:, site])
+        hout = hist_all.copy()
+        lib.ndo_engram_conv(hist_all.ctypes.data, _f(value).ctypes.data, rs.ctypes.data, count, taps.ctypes.data,
+                            g["engram_dilation"], dim, conv.ctypes.data, hout.ctypes.data)
+        self.ehist[:, site] = hout
+        for t in range(count):
+            lib.ndo_engram_gate(_f(u[t]).ctypes.data, _f(key[t]).ctypes.data, conv[t].ctypes.data, dim,
+                                residual[t].ctypes.data)
+
+    def _attention(self, l, slots, residual):
+        g, lib = self.g, O.lib()
+        count, dim = len(slots), self.dim
+        H, KV, QK, VD = g["heads"], g["kv_heads"], g["qk_dim"], g["v_dim"]
+        norm_in = _f(self.dense("layer.norm_in", l))
+        x = np.stack([O.fake_a8_row(1, residual[t], norm_in) for t in range(count)])
+        act = O.prepare_cq(x, 2)
+        q, k, v = self._matmul("layer.q", l, act), self._matmul("layer.k", l, act), self._matmul("layer.v", l, act)
+        gate = self._matmul("layer.gate", l, act)
+        out = np.zeros((count, self.ow), np.float32)
+        qtaps, ktaps, vtaps = (_f(self.dense("layer." + n, l)) for n in ("q_taps", "k_taps", "v_taps"))
+        qn, kn = _f(self.dense("layer.q_norm", l)), _f(self.dense("layer.k_norm", l))
+        window = 0 if (g["global_mask"] >> l) & 1 else g["sliding_window"]
+        inv_sqrt = np.float32(1.0) / np.float32(np.sqrt(np.float32(QK)))
+        for t, s in enumerate(slots):
+            p = int(self.length[s])
+            conv = []
+            for hist, cur, taps, w in ((self.qhist, q[t], qtaps, self.qw), (self.khist, k[t], ktaps, self.kw),
+                                       (self.vhist, v[t], vtaps, self.vw)):
+                triple = _f(np.concatenate([hist[s, l, 0], hist[s, l, 1], cur]))
+                o = np.zeros(w, np.float32)
+                lib.ndo_taps3(taps.ctypes.data, w, triple[2 * w:].ctypes.data, o.ctypes.data)
+                conv.append(o)
+                hist[s, l, 0] = hist[s, l, 1]
+                hist[s, l, 1] = cur
+            qc, kc, vc = conv
+            for h in range(H):
+                seg = _f(qc[h * QK:(h + 1) * QK])
+                lib.ndo_zero_centered_rms(seg.ctypes.data, qn.ctypes.data, QK, seg.ctypes.data)
+                qc[h * QK:(h + 1) * QK] = seg
+            for h in range(KV):
+                seg = _f(kc[h * QK:(h + 1) * QK])
+                lib.ndo_zero_centered_rms(seg.ctypes.data, kn.ctypes.data, QK, seg.ctypes.data)
+                kc[h * QK:(h + 1) * QK] = seg
+            cos, sin = _f(self.cos[p]), _f(self.sin[p])
+            lib.ndo_rope(qc.ctypes.data, H, QK, cos.ctypes.data, sin.ctypes.data)
+            lib.ndo_rope(kc.ctypes.data, KV, QK, cos.ctypes.data, sin.ctypes.data)
+            q8 = np.zeros(self.qw, np.int8)
+            qs = np.zeros(H, np.float32)
+            for h in range(H):
+                q8[h * QK:(h + 1) * QK], qs[h] = O.quantize_int8(qc[h * QK:(h + 1) * QK])
+            for h in range(KV):
+                self.keys[s, l, p, h * QK:(h + 1) * QK], self.kscale[s, l, p, h] = O.quantize_int8(
+                    kc[h * QK:(h + 1) * QK])
+                self.values[s, l, p, h * VD:(h + 1) * VD], self.vscale[s, l, p, h] = O.quantize_int8(
+                    vc[h * VD:(h + 1) * VD])
+            first = 0 if window == 0 else max(0, p - window + 1)
+            group = H // KV
+            for h in range(H):
+                kvh = h // group
+                keys = np.ascontiguousarray(self.keys[s, l, :, kvh * QK:(kvh + 1) * QK])
+                vals = np.ascontiguousarray(self.values[s, l, :, kvh * VD:(kvh + 1) * VD])
+                ks = np.ascontiguousarray(self.kscale[s, l, :, kvh])
+                vs = np.ascontiguousarray(self.vscale[s, l, :, kvh])
+                out[t, h * VD:(h + 1) * VD] = O.attention_head(
+                    np.ascontiguousarray(q8[h * QK:(h + 1) * QK]), float(qs[h]), keys, ks, vals, vs, QK, VD, 1,
+                    first, p, QK, VD, float(inv_sqrt))
+        gated = np.stack([O.fake_a8_row(2, out[t], gate[t]) for t in range(count)])
+        proj = self._matmul("layer.out", l, O.prepare_cq(gated, 2))
+        post_norm = _f(self.dense("layer.post_norm", l))
+        attn_gate = float(O.lib().ndo_sigmoid(float(self.dense("layer.attn_gate", l)[0])))
+        for t in range(count):
+            lib.ndo_post_norm_add(residual[t].ctypes.data, _f(proj[t]).ctypes.data, post_norm.ctypes.data,
+                                  attn_gate, dim)
+
+    def _mlp(self, l, residual):
+        g = self.g
+        names = ["d1", "d2", "b2", "d3", "d4", "w1a", "w1b", "w2a", "w2b", "w3a", "w3b", "cond_v", "cond_u"]
+        host = [_f(self.dense("layer.mlp." + n, l)) for n in names]
+        ptrs = (ctypes.c_void_p * 13)(*[h.ctypes.data for h in host])
+        pre = _f(self.dense("layer.pre_hada", l))
+        pa = np.ascontiguousarray(self.perm("hyper.perm_a"), np.int32)
+        pb = np.ascontiguousarray(self.perm("hyper.perm_b"), np.int32)
+        for t in range(residual.shape[0]):
+            O.lib().ndo_hadamard_mlp(ptrs, pre.ctypes.data, pa.ctypes.data, pb.ctypes.data, self.dim, g["hada_rows"],
+                                     g["hada_cols"], 1.0, residual[t].ctypes.data)
+
+    # -- the step --
+    def forward(self, tokens, slots, head_rows=()):
+        """One ForwardBatch over rows of distinct slots; returns logits
+        [len(head_rows)][vocab]."""
+        g, lib = self.g, O.lib()
+        tokens = np.asarray(tokens, np.int32)
+        slots = [int(s) for s in slots]
+        assert len(set(slots)) == len(slots), "rows of one forward are distinct slots"
+        count, dim = len(slots), self.dim
+        codes, norms, _, _, bits = self.cq("embedding", 0)
+        scale = np.float32(np.sqrt(np.float32(dim))) - np.float32(1.0)
+        stream = np.zeros((count, LANES, dim), np.float32)
+        for t in range(count):
+            x = O.gather_row_cq(codes, norms, self.levels4, bits, int(tokens[t]))
+            x = (x + scale * x).astype(np.float32)  # AddScaled(x, x, sqrt(dim) - 1): x + s*x, two roundings
+            stream[t, :] = x
+        a_pre, b_pre = _f(self.dense("hyper.a_pre")), _f(self.dense("hyper.b_pre"))
+        a_post, b_post = _f(self.dense("hyper.a_post")), _f(self.dense("hyper.b_post"))
+        a_res, b_res = _f(self.dense("hyper.a_res")), _f(self.dense("hyper.b_res"))
+        sig = lambda v: np.float32(lib.ndo_sigmoid(float(v)))
+        for l in range(g["layers"]):
+            lane = l % LANES
+            flat = stream.reshape(count, LANES * dim)
+            norm = np.stack([O.fake_a8_row(0, flat[t]) for t in range(count)])
+            act = O.prepare_cq(norm, 4)
+            pre = self._matmul("hyper.phi_pre", 0, act, (l * LANES, l * LANES + LANES))
+            post = self._matmul("hyper.phi_post", 0, act, (l * LANES, l * LANES + LANES))
+            res = self._matmul("hyper.phi_res", 0, act, (l * 16, l * 16 + 16))
+            u = np.zeros((count, dim), np.float32)
+            mix = np.zeros((count, 16), np.float32)
+            post_gate = np.zeros((count, LANES), np.float32)
+            for t in range(count):
+                hpre = np.zeros(LANES, np.float32)
+                for i in range(LANES):
+                    zp = np.float32(np.float32(a_pre[l] * pre[t, i]) + b_pre[l * LANES + i]) + np.float32(
+                        4.0 if i == lane else -4.0)
+                    hpre[i] = sig(zp)
+                    zq = np.float32(np.float32(a_post[l] * post[t, i]) + b_post[l * LANES + i]) + np.float32(
+                        0.0 if i == lane else -4.0)
+                    post_gate[t, i] = np.float32(2.0) * sig(zq)
+                lib.ndo_mix4(stream[t].ctypes.data, dim, float(hpre[0]), float(hpre[1]), float(hpre[2]),
+                             float(hpre[3]), u[t].ctypes.data)
+                logits = _f([np.float32(a_res[l] * res[t, i]) + b_res[l * 16 + i] for i in range(16)])
+                mix[t] = O.sinkhorn4x4(logits)
+            residual = u.copy()
+            site = self._site(l)
+            if site >= 0:
+                self._engram(site, tokens, slots, u, residual)
+            self._attention(l, slots, residual)
+            self._mlp(l, residual)
+            nxt = np.zeros_like(stream)
+            for t in range(count):
+                lib.ndo_combine_diff4x4(stream[t].ctypes.data, dim, mix[t].ctypes.data, residual[t].ctypes.data,
+                                        u[t].ctypes.data, post_gate[t].ctypes.data, nxt[t].ctypes.data)
+            stream = nxt
+        for t, s in enumerate(slots):
+            self.prev[s, 0], self.prev[s, 1] = self.prev[s, 1], tokens[t]
+            self.length[s] += 1
+        final_norm = _f(self.dense("final_norm"))
+        out = []
+        for r in head_rows:
+            mean = np.zeros(dim, np.float32)
+            lib.ndo_mix4(stream[r].ctypes.data, dim, 0.25, 0.25, 0.25, 0.25, mean.ctypes.data)
+            nz = np.zeros(dim, np.float32)
+            lib.ndo_zero_centered_rms(mean.ctypes.data, final_norm.ctypes.data, dim, nz.ctypes.data)
+            lib.ndo_fake_a8(nz.ctypes.data, dim)
+            out.append(self._matmul("embedding", 0, O.prepare_cq(nz[None, :], 4))[0])
+        self.last_stream = stream
+        vocab = self.cq("embedding", 0)[2]
+        return np.array(out, np.float32).reshape(len(head_rows), vocab)

@@ -174,3 +174,56 @@ class Archive:
             blobs += payload
             at += len(payload)
         return h.tobytes() + self.levels.tobytes() + table + blobs
+
+
+def needle3_decoder_archive(seed=0, **geometry):
+    """A complete Needle-3 archive whose shapes drive a whole decode step
+    (the phi matrices cover every layer, the projections have their head
+    shapes) with tame values: unit-scale norms near zero, small conv taps
+    and MLP factors, so activations stay finite through the layers."""
+    g = dict(GEOMETRY, dim=512, heads=2, kv_heads=1, qk_dim=48, v_dim=64, layers=2, vocab=384, hada_n=512,
+             engram_sub=128, engram_tables=4, engram_slots=97, orders=[2, 3], sites=[1], sliding_window=8,
+             global_mask=0b10, max_seq=512)
+    g.update(geometry)
+    a = Archive(seed=seed, geometry=g)
+    rng = a.rng
+    d, L = g["dim"], g["layers"]
+    qw, kw, vw, ow = g["heads"] * g["qk_dim"], g["kv_heads"] * g["qk_dim"], g["kv_heads"] * g["v_dim"], \
+        g["heads"] * g["v_dim"]
+
+    def small(n, sd):
+        return rng.normal(0, sd, n).astype(np.float16).view(np.uint16)
+
+    a.cq("embedding", 0, g["vocab"], d, 4)
+    sizes = {"layer.norm_in": d, "layer.q_taps": 3 * qw, "layer.k_taps": 3 * kw, "layer.v_taps": 3 * vw,
+             "layer.q_norm": g["qk_dim"], "layer.k_norm": g["qk_dim"], "layer.post_norm": d, "layer.pre_hada": d}
+    shapes = {"layer.q": (qw, d), "layer.k": (kw, d), "layer.v": (vw, d), "layer.gate": (ow, d), "layer.out": (d, ow)}
+    for layer in range(L):
+        for item in LAYER:
+            role = item[0] if isinstance(item, tuple) else item
+            if role in shapes:
+                a.cq(role, layer, shapes[role][0], shapes[role][1], 2)
+            elif role == "layer.attn_gate":
+                a.dense(role, layer, 1, fp16=False, values=rng.normal(0, 1, 1).astype(np.float32))
+            elif role.startswith("layer.mlp."):
+                n = a._layer_size(role)
+                sd = 0.1 if role.rsplit(".", 1)[1].startswith(("w", "cond")) else 0.3
+                a.dense(role, layer, n, values=small(n, sd))
+            else:
+                sd = 0.5 if role.endswith("taps") else 0.1
+                a.dense(role, layer, sizes[role], values=small(sizes[role], sd))
+    for n, count in (("a_pre", L), ("a_post", L), ("a_res", L), ("b_pre", 4 * L), ("b_post", 4 * L),
+                     ("b_res", 16 * L)):
+        a.dense("hyper." + n, 0, count, values=small(count, 0.5))
+    for n, rows in (("phi_pre", 4 * L), ("phi_post", 4 * L), ("phi_res", 16 * L)):
+        a.cq("hyper." + n, 0, rows, 4 * d, 4)
+    a.perm("hyper.perm_a", g["hada_n"])
+    a.perm("hyper.perm_b", g["hada_n"])
+    for s in range(len(g["sites"])):
+        a.cq("site.tables", s, g["engram_tables"] * g["engram_slots"], g["engram_sub"], 4)
+        a.cq("site.key", s, d, d, 2)
+        a.cq("site.value", s, d, d, 2)
+        a.dense("site.taps", s, 4 * d, values=small(4 * d, 0.3))
+    a.dense("final_norm", 0, d, values=small(d, 0.1))
+    a.raw(b"needle tokenizer blob \x00\x01\x02")
+    return a
