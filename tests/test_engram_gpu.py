@@ -3,9 +3,9 @@
 the slot history and the residual gate (ApplyEngramBatch, :2405-2469),
 against the oracle's scalar restatements.
 
-Bars: hash rows and conv outputs (and the new slot histories) bit-exact; the
-gate within 1e-6 of the residual update scale (its sigmoid goes through
-CUDA's expf).  Batches mix decode rows (runs of one) with prefill runs of
+Bar: hash rows, conv outputs, the new slot histories and the gated residual
+bit-exact (the gate's sigmoid takes the correctly rounded exponential on
+both sides).  Batches mix decode rows (runs of one) with prefill runs of
 several tokens of one slot, including slots too short for an n-gram.
 """
 import numpy as np
@@ -107,5 +107,5 @@ def test_engram_gate_matches_oracle(dev, oracle):
     _native.call("ndl_engram_gate", dx.data_ptr(), dk.data_ptr(), dv.data_ptr(), count, dim, dres.data_ptr(), None)
     torch.cuda.synchronize()
     got = dres.cpu().numpy()
-    assert np.abs(got - want).max() <= 1e-6 * np.abs(v).max() + 1e-6 * np.abs(want).max()
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), np.abs(got - want).max()
     assert np.abs(want - res).max() > 0.1  # the gate is open enough to matter

@@ -9,7 +9,8 @@ directly, each checked bit for bit against the oracle:
  * an embedding gather (ndl_cq_gather_rows on "embedding");
  * a CQ matmul (ndl_cq_matmul on "layer.gate" 1 with the model's codebook);
  * the confidence head (ndl_conf_pool_update and ndl_conf_logit on the
-   probe head's tensors), to the oracle's tolerance for its exp.
+   probe head's tensors), bit for bit as well (MathF.Exp is the correctly
+   rounded exponential on both sides).
 """
 import ctypes
 
@@ -167,14 +168,14 @@ def test_confidence_head_runs_on_model_weights(loaded, oracle):
         wp = np.zeros((queries, dim), np.float32)
         wl = olib.ndo_conf_logit(want[2][s].ctypes.data, want[3][s].ctypes.data, pool_rows, dim, gain.ctypes.data,
                                  qv.ctypes.data, rb.ctypes.data, bias, proj.ctypes.data, queries, wp.ctypes.data)
-        assert abs(got[r] - wl) <= 1e-5 * max(1.0, abs(wl)), (r, got[r], wl)
+        assert np.float32(got[r]) == np.float32(wl), (r, got[r], wl)
 
 
 def test_kronecker_mlp_runs_on_model_weights(loaded, oracle):
     """ndl_mlp_apply over several residual rows of a layer against the oracle's
-    HadamardMlp restatement on the same (host) tensors, to the KernelTable
-    slot's bar (2e-5 of the update: the condition softmax and the SiLU go
-    through expf)."""
+    HadamardMlp restatement on the same (host) tensors, bit for bit (the
+    condition softmax and the SiLU take the correctly rounded exponential on
+    both sides)."""
     import torch
 
     from needle_cs_b200 import _native
@@ -199,4 +200,4 @@ def test_kronecker_mlp_runs_on_model_weights(loaded, oracle):
         got = res.cpu().numpy()
         delta = np.abs(want - residual).max()
         assert delta > 1e-3  # the MLP moves the rows
-        assert np.abs(got - want).max() <= 2e-5 * max(1.0, float(delta)), np.abs(got - want).max()
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), np.abs(got - want).max()
