@@ -555,7 +555,8 @@ NDL_API int ndl_slot_copy(ndl_engine *e, int dst, int src);
  * layout: int32 length, then per layer keys int8 [len][heads*64], values
  * int8 [len][heads*64], key scales fp32 [len][heads], value scales fp32
  * [len][heads] (the synthetic decoders keep no recurrent engine state, so
- * the reference's state section is empty).  Import replaces the slot's cache
+ * the reference's state section is empty; a Needle-3 engine's blob carries
+ * it, see ndl_engine_create_model).  Import replaces the slot's cache
  * and sets its length and mark to the blob's length; a short buffer or blob
  * and a length beyond the capacity are NDL_ERR_INVALID_ARG. */
 NDL_API int ndl_slot_prefix_bytes(ndl_engine *e, int slot, size_t *bytes);
@@ -809,10 +810,17 @@ NDL_API int ndl_engram_apply(const ndl_model *m, int site, const int32_t *tokens
  * A run of rows of one slot is equivalent to feeding them one at a time, and
  * is computed that way.  Slot state (lengths, previous tokens, conv and
  * Engram histories, K / V cache) is per slot on the device; ndl_slot_reset
- * clears it.  Sampling, masks, top-k and ndl_batch_logits_row work as on
- * the synthetic decoder.  Not available on this engine (NDL_ERR_UNSUPPORTED):
- * mark / rewind, slot copies, prefixes, cross memory, the sparse head, the
- * tensor views and the attention timer.  The model must stay loaded while
+ * clears it, ndl_slot_mark / ndl_slot_rewind keep and restore it
+ * (MarkView / RewindView, src/Needle/Engine.cs:2235-2255), and the primed-
+ * prefix calls move a slot's marked prefix as the reference's blob with its
+ * state section: int32 length; per layer the conv histories q | k | v (two
+ * entries each, fp32); per Engram site the 9-entry history; the previous two
+ * tokens; the confidence pools at their reset values (this engine does not
+ * pool); then per layer keys [len][kv*qk], values [len][kv*v], key and value
+ * scales [len][kv].  Sampling, masks, top-k and ndl_batch_logits_row work as
+ * on the synthetic decoder.  Not available on this engine
+ * (NDL_ERR_UNSUPPORTED): slot copies and shared prefixes, cross memory, the
+ * sparse head, the page / tensor views and the attention timer.  The model must stay loaded while
  * the engine lives; capacity is at most 8192 and the model's head dims at
  * most 64. */
 NDL_API int ndl_engine_create_model(const ndl_engine_config *engine, const ndl_model *model, ndl_engine **out);

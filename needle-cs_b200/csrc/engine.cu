@@ -834,8 +834,12 @@ NDL_API int ndl_slot_reset(ndl_engine *e, int slot) {
 
 // EngineCore.MarkSlot (src/Needle/Engine.cs:2273-2277): remember the length.
 NDL_API int ndl_slot_mark(ndl_engine *e, int slot) {
-    if (e && e->n3) return set_error(NDL_ERR_UNSUPPORTED, "%s: not available on a Needle-3 engine", "ndl_slot_mark");
     TRY(check_slot(e, slot));
+    if (e->n3) {
+        TRY(ndl::n3_mark(e->n3, slot, e->stream));
+        e->slot_mark[slot] = e->slot_len[slot];
+        return NDL_OK;
+    }
     e->slot_mark[slot] = e->slot_len[slot];
     return NDL_OK;
 }
@@ -843,8 +847,12 @@ NDL_API int ndl_slot_mark(ndl_engine *e, int slot) {
 // EngineCore.RewindSlot (src/Needle/Engine.cs:2279-2283): back to the mark;
 // pages wholly past the mark are returned to the pool.
 NDL_API int ndl_slot_rewind(ndl_engine *e, int slot) {
-    if (e && e->n3) return set_error(NDL_ERR_UNSUPPORTED, "%s: not available on a Needle-3 engine", "ndl_slot_rewind");
     TRY(check_slot(e, slot));
+    if (e->n3) {
+        TRY(ndl::n3_rewind(e->n3, slot, e->stream));
+        e->slot_len[slot] = e->slot_mark[slot];
+        return NDL_OK;
+    }
     std::vector<int32_t> updates;
     int keep = (e->slot_mark[slot] + kPagePositions - 1) / kPagePositions;
     free_slot_pages(e, slot, keep, &updates);
@@ -1216,9 +1224,12 @@ NDL_API int ndl_engine_free_pages(ndl_engine *e, int *free_pages) {
 // Engine.PrimedPrefixBytes (src/Needle/Engine.cs:398-400): bytes of the blob
 // of the slot's marked prefix (its length at ndl_slot_mark).
 NDL_API int ndl_slot_prefix_bytes(ndl_engine *e, int slot, size_t *bytes) {
-    if (e && e->n3) return set_error(NDL_ERR_UNSUPPORTED, "%s: not available on a Needle-3 engine", "ndl_slot_prefix_bytes");
     NDL_REQUIRE(e && bytes, "null argument");
     TRY(check_slot(e, slot));
+    if (e->n3) {
+        *bytes = ndl::n3_prefix_bytes(e->n3, e->slot_mark[slot]);
+        return NDL_OK;
+    }
     *bytes = prefix_blob_bytes(e->dc.layers, e->dc.heads, e->slot_mark[slot]);
     return NDL_OK;
 }
@@ -1226,10 +1237,15 @@ NDL_API int ndl_slot_prefix_bytes(ndl_engine *e, int slot, size_t *bytes) {
 // Engine.ExportPrimedPrefix (src/Needle/Engine.cs:402-427): the slot's
 // marked prefix as a blob (layout in prefix.cu).
 NDL_API int ndl_slot_export_prefix(ndl_engine *e, int slot, void *blob, size_t bytes) {
-    if (e && e->n3) return set_error(NDL_ERR_UNSUPPORTED, "%s: not available on a Needle-3 engine", "ndl_slot_export_prefix");
     NDL_REQUIRE(e && blob, "null argument");
     TRY(check_slot(e, slot));
     const int len = e->slot_mark[slot];
+    if (e->n3) {
+        const size_t n3_need = ndl::n3_prefix_bytes(e->n3, len);
+        NDL_REQUIRE(bytes >= n3_need, "primed prefix buffer too small (%zu bytes, %zu needed)", bytes, n3_need);
+        *static_cast<int32_t *>(blob) = len;
+        return ndl::n3_prefix_move(e->n3, slot, true, static_cast<uint8_t *>(blob), len, e->stream);
+    }
     const size_t need = prefix_blob_bytes(e->dc.layers, e->dc.heads, len);
     NDL_REQUIRE(bytes >= need, "primed prefix buffer too small (%zu bytes, %zu needed)", bytes, need);
     *static_cast<int32_t *>(blob) = len;
@@ -1247,12 +1263,19 @@ NDL_API int ndl_slot_export_prefix(ndl_engine *e, int slot, void *blob, size_t b
 // Engine.ImportPrimedPrefix (src/Needle/Engine.cs:429-464): the slot's cache
 // becomes the blob's prefix; its length and mark are the blob's length.
 NDL_API int ndl_slot_import_prefix(ndl_engine *e, int slot, const void *blob, size_t bytes) {
-    if (e && e->n3) return set_error(NDL_ERR_UNSUPPORTED, "%s: not available on a Needle-3 engine", "ndl_slot_import_prefix");
     NDL_REQUIRE(e && blob, "null argument");
     TRY(check_slot(e, slot));
     NDL_REQUIRE(bytes >= 4, "primed prefix is truncated");
     const int len = *static_cast<const int32_t *>(blob);
     NDL_REQUIRE(len >= 0 && len <= e->ec.capacity, "primed prefix length exceeds context capacity");
+    if (e->n3) {
+        NDL_REQUIRE(bytes >= ndl::n3_prefix_bytes(e->n3, len), "primed prefix is truncated");
+        TRY(ndl_slot_reset(e, slot));
+        TRY(ndl::n3_prefix_move(e->n3, slot, false, static_cast<uint8_t *>(const_cast<void *>(blob)), len, e->stream));
+        e->slot_len[slot] = len;
+        e->slot_mark[slot] = len;
+        return NDL_OK;
+    }
     const size_t need = prefix_blob_bytes(e->dc.layers, e->dc.heads, len);
     NDL_REQUIRE(bytes >= need, "primed prefix is truncated");
     TRY(ndl_slot_reset(e, slot));

@@ -87,7 +87,11 @@ struct N3State {
     int act_stride = 0;
     void *engram_ws = nullptr;
     size_t engram_ws_bytes = 0;
-    std::vector<int> host_len;
+    std::vector<int> host_len, host_mark;
+    // each slot's state at its mark (MarkSlot / RewindSlot): conv and Engram histories, previous tokens
+    float *snap_conv = nullptr, *snap_ehist = nullptr;
+    int32_t *snap_prev = nullptr;
+    int pool_rows = 0;  // the confidence head's pool rows the reference's state carries (this engine does not pool)
 };
 
 namespace {
@@ -609,10 +613,118 @@ int n3_reset_slot(N3State *s, int slot, cudaStream_t st) {
         NDL_CUDA(cudaMemsetAsync(s->ehist[0] + ((size_t)site * s->slots + slot) * kEngramHistory * d, 0,
                                  (size_t)kEngramHistory * d * 4, st));
     s->host_len[slot] = 0;
-    return NDL_OK;
+    s->host_mark[slot] = 0;
+    return n3_mark(s, slot, st);  // the reset state is also the mark's
 }
 
 int n3_slot_length(const N3State *s, int slot) { return s->host_len[slot]; }
+
+// The slot's live (or snapshot) histories: conv [L][2][width], each site's
+// Engram [9][dim], previous tokens [2], copied one way or the other.
+static int copy_state(N3State *s, int slot, bool to_snapshot, cudaStream_t st) {
+    const int L = s->layers, width = s->qw + s->kw + s->vw, d = s->dim;
+    const size_t conv = (size_t)L * kConvHist * width;
+    float *live_c = s->conv_hist + (size_t)slot * conv, *snap_c = s->snap_conv + (size_t)slot * conv;
+    NDL_CUDA(cudaMemcpyAsync(to_snapshot ? snap_c : live_c, to_snapshot ? live_c : snap_c, conv * 4,
+                             cudaMemcpyDeviceToDevice, st));
+    for (int site = 0; site < s->sites; site++) {
+        const size_t at = ((size_t)site * s->slots + slot) * kEngramHistory * d;
+        NDL_CUDA(cudaMemcpyAsync(to_snapshot ? s->snap_ehist + at : s->ehist[0] + at,
+                                 to_snapshot ? s->ehist[0] + at : s->snap_ehist + at, (size_t)kEngramHistory * d * 4,
+                                 cudaMemcpyDeviceToDevice, st));
+    }
+    NDL_CUDA(cudaMemcpyAsync(to_snapshot ? s->snap_prev + 2 * slot : s->prev + 2 * slot,
+                             to_snapshot ? s->prev + 2 * slot : s->snap_prev + 2 * slot, 8, cudaMemcpyDeviceToDevice,
+                             st));
+    return NDL_OK;
+}
+
+__global__ void n3_set_length_kernel(int32_t *len, int slot, int value) { len[slot] = value; }
+
+// MarkView (src/Needle/Engine.cs:2235-2244): the histories and previous
+// tokens as they are now, and the length.
+int n3_mark(N3State *s, int slot, cudaStream_t st) {
+    if (slot < 0 || slot >= s->slots) return set_error(NDL_ERR_INVALID_ARG, "slot %d", slot);
+    N3_TRY(copy_state(s, slot, true, st));
+    s->host_mark[slot] = s->host_len[slot];
+    return NDL_OK;
+}
+
+// RewindView (:2246-2255): back to the mark's histories, previous tokens and
+// length (cache positions past it are rewritten by later forwards).
+int n3_rewind(N3State *s, int slot, cudaStream_t st) {
+    if (slot < 0 || slot >= s->slots) return set_error(NDL_ERR_INVALID_ARG, "slot %d", slot);
+    N3_TRY(copy_state(s, slot, false, st));
+    s->host_len[slot] = s->host_mark[slot];
+    n3_set_length_kernel<<<1, 1, 0, st>>>(s->len, slot, s->host_mark[slot]);
+    return check_launch("n3_set_length");
+}
+
+int n3_slot_mark(const N3State *s, int slot) { return s->host_mark[slot]; }
+
+// Engine.PrimedPrefixBytes (src/Needle/Engine.cs:398-400) for a marked length:
+// int32 length, the state (stateBytes: conv histories, Engram histories,
+// previous tokens, the confidence pools), then per layer the cache rows.
+size_t n3_prefix_bytes(const N3State *s, int len) {
+    const size_t width = (size_t)s->qw + s->kw + s->vw;
+    const size_t state = ((size_t)s->layers * kConvHist * width + (size_t)s->sites * kEngramHistory * s->dim + 2 +
+                          (size_t)s->pool_rows * (s->dim + 2)) * 4;
+    return 4 + state + (size_t)s->layers * len * (s->kw + s->vw + 2 * (size_t)s->kv * 4);
+}
+
+// ExportPrimedPrefix / ImportPrimedPrefix (src/Needle/Engine.cs:402-464) on
+// one slot: the state section is the slot's marked state (the pools at their
+// reset values: this engine keeps no confidence pools), then for each layer
+// the first `len` cache positions: keys [len][kw], values [len][vw], key and
+// value scales [len][kv].  Each piece is one copy between host and device.
+int n3_prefix_move(N3State *s, int slot, bool to_blob, uint8_t *blob, int len, cudaStream_t st) {
+    const int L = s->layers, width = s->qw + s->kw + s->vw, d = s->dim;
+    const cudaMemcpyKind kind = to_blob ? cudaMemcpyDeviceToHost : cudaMemcpyHostToDevice;
+    auto move = [&](void *dev, uint8_t *host, size_t bytes) -> int {
+        if (bytes == 0) return NDL_OK;
+        cudaError_t e = to_blob ? cudaMemcpyAsync(host, dev, bytes, kind, st) : cudaMemcpyAsync(dev, host, bytes, kind, st);
+        return e == cudaSuccess ? NDL_OK : set_error(NDL_ERR_CUDA, "primed prefix copy: %s", cudaGetErrorString(e));
+    };
+    uint8_t *at = blob + 4;
+    const size_t conv = (size_t)L * kConvHist * width;
+    // state: the snapshot on export; on import both the live state and the snapshot
+    N3_TRY(move(s->snap_conv + (size_t)slot * conv, at, conv * 4));
+    at += conv * 4;
+    for (int site = 0; site < s->sites; site++) {
+        N3_TRY(move(s->snap_ehist + ((size_t)site * s->slots + slot) * kEngramHistory * d, at,
+                    (size_t)kEngramHistory * d * 4));
+        at += (size_t)kEngramHistory * d * 4;
+    }
+    N3_TRY(move(s->snap_prev + 2 * slot, at, 8));
+    at += 8;
+    if (to_blob) {
+        float *pool = reinterpret_cast<float *>(at);
+        for (int i = 0; i < s->pool_rows; i++) pool[i] = -1e30f;  // ResetView's pool maxima
+        memset(pool + s->pool_rows, 0, (size_t)s->pool_rows * (d + 1) * 4);
+    }
+    at += (size_t)s->pool_rows * (d + 2) * 4;
+    for (int l = 0; l < L; l++) {
+        const size_t base = ((size_t)slot * L + l) * s->capacity;
+        N3_TRY(move(s->keys + base * s->kw, at, (size_t)len * s->kw));
+        at += (size_t)len * s->kw;
+        N3_TRY(move(s->values + base * s->vw, at, (size_t)len * s->vw));
+        at += (size_t)len * s->vw;
+        N3_TRY(move(s->kscale + base * s->kv, at, (size_t)len * s->kv * 4));
+        at += (size_t)len * s->kv * 4;
+        N3_TRY(move(s->vscale + base * s->kv, at, (size_t)len * s->kv * 4));
+        at += (size_t)len * s->kv * 4;
+    }
+    if (!to_blob) {
+        N3_TRY(copy_state(s, slot, false, st));  // the live state starts as the blob's
+        s->host_len[slot] = s->host_mark[slot] = len;
+        n3_set_length_kernel<<<1, 1, 0, st>>>(s->len, slot, len);
+        N3_TRY(check_launch("n3_set_length"));
+    }
+    NDL_CUDA(cudaStreamSynchronize(st));  // the host blob is complete (export) or consumed (import)
+    return NDL_OK;
+}
+
+int n3_capacity(const N3State *s) { return s->capacity; }
 
 int n3_create(const ndl_model *m, int slots, int capacity, int max_rows, int max_heads, cudaStream_t st,
               N3State **out) {
@@ -733,6 +845,15 @@ int n3_create(const ndl_model *m, int slots, int capacity, int max_rows, int max
         (rc = n3_alloc(s, &s->act_offsets, (size_t)R * s->act_stride)) != NDL_OK ||
         (rc = n3_alloc(s, &s->q8, (size_t)R * s->qw)) != NDL_OK || (rc = n3_alloc(s, &s->qs, (size_t)R * s->heads)) != NDL_OK)
         return fail(rc);
+    if ((rc = n3_alloc(s, &s->snap_conv, (size_t)slots * L * kConvHist * width)) != NDL_OK ||
+        (rc = n3_alloc(s, &s->snap_ehist, (size_t)std::max(s->sites, 1) * slots * kEngramHistory * d)) != NDL_OK ||
+        (rc = n3_alloc(s, &s->snap_prev, (size_t)slots * 2)) != NDL_OK)
+        return fail(rc);
+    if (info.confidence_head >= 0) {
+        ndl_model_tensor pv;
+        if (ndl_model_get_tensor(m, "probe.probe_vectors", info.confidence_head, &pv) == NDL_OK && L + 1 > 0)
+            s->pool_rows = (pv.rows / (L + 1)) * (L + 1);
+    }
     if (cudaMallocHost(&s->h_rows, (size_t)3 * R * sizeof(int32_t)) != cudaSuccess)
         return fail(set_error(NDL_ERR_OUT_OF_MEMORY, "Needle-3 staging"));
     s->engram_ws_bytes = s->sites > 0 ? ndl_engram_workspace(m, R) : 0;
@@ -750,6 +871,10 @@ int n3_create(const ndl_model *m, int slots, int capacity, int max_rows, int max
         cudaMemcpy(s->gate_rows, g.data(), g.size() * 4, cudaMemcpyHostToDevice);
     }
     s->host_len.assign(slots, 0);
+    s->host_mark.assign(slots, 0);
+    NDL_CUDA(cudaMemsetAsync(s->snap_conv, 0, (size_t)slots * L * kConvHist * width * 4, st));
+    NDL_CUDA(cudaMemsetAsync(s->snap_ehist, 0, (size_t)std::max(s->sites, 1) * slots * kEngramHistory * d * 4, st));
+    NDL_CUDA(cudaMemsetAsync(s->snap_prev, 0, (size_t)slots * 8, st));
     NDL_CUDA(cudaMemsetAsync(s->len, 0, (size_t)slots * 4, st));
     NDL_CUDA(cudaMemsetAsync(s->prev, 0, (size_t)slots * 8, st));
     NDL_CUDA(cudaMemsetAsync(s->conv_hist, 0, (size_t)slots * L * kConvHist * width * 4, st));

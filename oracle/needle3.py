@@ -86,12 +86,49 @@ class Needle3Oracle:
         self.values = np.zeros((S, L, C, self.vw), np.int8)
         self.vscale = np.zeros((S, L, C, g["kv_heads"]), np.float32)
         self.ehist = np.zeros((S, max(g["site_count"], 1), ENGRAM_HISTORY, self.dim), np.float32)
+        self.snap = {}
+        for s in range(S):
+            self.mark(s)
 
     def reset_slot(self, s):
         for a in (self.qhist, self.khist, self.vhist, self.keys, self.kscale, self.values, self.vscale, self.ehist,
                   self.prev):
             a[s] = 0
         self.length[s] = 0
+        self.mark(s)
+
+    # MarkView / RewindView (src/Needle/Engine.cs:2235-2255): the histories,
+    # previous tokens and length at the mark
+    def mark(self, s):
+        if not hasattr(self, "snap"):
+            self.snap = {}
+        self.snap[s] = (self.qhist[s].copy(), self.khist[s].copy(), self.vhist[s].copy(), self.ehist[s].copy(),
+                        self.prev[s].copy(), int(self.length[s]))
+
+    def rewind(self, s):
+        q, k, v, e, p, n = self.snap[s]
+        self.qhist[s], self.khist[s], self.vhist[s], self.ehist[s], self.prev[s] = q, k, v, e, p
+        self.length[s] = n
+
+    def prefix_blob(self, s, pool_rows=0):
+        """ExportPrimedPrefix (src/Needle/Engine.cs:402-427) of slot s's mark:
+        int32 length, the state (per layer the conv histories q | k | v, two
+        entries each; per site the Engram history; the previous two tokens;
+        the confidence pools at their reset values), then per layer keys,
+        values, key scales and value scales of the marked positions."""
+        q, k, v, e, p, n = self.snap[s]
+        parts = [np.array([n], np.int32).tobytes()]
+        for l in range(self.g["layers"]):
+            parts += [q[l].tobytes(), k[l].tobytes(), v[l].tobytes()]
+        for site in range(self.g["site_count"]):
+            parts.append(e[site].tobytes())
+        parts.append(p.astype(np.int32).tobytes())
+        parts.append(np.full(pool_rows, -1e30, np.float32).tobytes() + np.zeros(pool_rows * (self.dim + 1),
+                                                                                 np.float32).tobytes())
+        for l in range(self.g["layers"]):
+            parts += [self.keys[s, l, :n].tobytes(), self.values[s, l, :n].tobytes(), self.kscale[s, l, :n].tobytes(),
+                      self.vscale[s, l, :n].tobytes()]
+        return b"".join(parts)
 
     # -- pieces --
     def _matmul(self, role, index, act, rows=None):

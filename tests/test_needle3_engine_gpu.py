@@ -102,6 +102,49 @@ def test_needle3_step_matches_the_scalar_chain(needle3, oracle):
         ids = got_ids
 
 
+def test_needle3_mark_rewind_and_primed_prefix(needle3, oracle):
+    """MarkSlot / RewindSlot restore the histories, previous tokens and length;
+    the primed-prefix blob carries the reference's state section (conv and
+    Engram histories, previous tokens) and the marked cache positions, byte
+    for byte the oracle's; a slot imported from it decodes exactly as the
+    slot it came from."""
+    a, m, eng = needle3
+    for s in range(SLOTS):
+        eng.reset_slot(s)
+    o = oracle_for(a, m, SLOTS, CAPACITY)
+    rng = np.random.default_rng(11)
+    V = m.info["vocab"]
+    prompt = [int(t) for t in rng.integers(0, V, 6)]
+    eng.forward_batch(prompt, [0] * 6, [5])
+    _oracle_batch(o, prompt, [0] * 6, [5])
+    eng.mark_slot(0)
+    o.mark(0)
+    for t in rng.integers(0, V, 3):  # decode past the mark, then back
+        eng.forward_batch([int(t)], [0], [0])
+        o.forward([int(t)], [0], [0])
+    eng.rewind_slot(0)
+    o.rewind(0)
+    assert eng.slot_length(0) == 6
+    blob = eng.export_prefix(0)
+    want = o.prefix_blob(0)
+    assert len(blob) == len(want) == eng.prefix_bytes(0)
+    assert blob == want
+    eng.import_prefix(3, blob)
+    assert eng.slot_length(3) == 6
+    o.reset_slot(3)
+    o.keys[3], o.values[3], o.kscale[3], o.vscale[3] = o.keys[0], o.values[0], o.kscale[0], o.vscale[0]
+    for name in ("qhist", "khist", "vhist", "ehist", "prev"):
+        getattr(o, name)[3] = getattr(o, name)[0]
+    o.length[3] = 6
+    for step in range(3):
+        tok = [int(t) for t in rng.integers(0, V, 1)] * 2
+        eng.forward_batch(tok, [0, 3], [0, 1])
+        got = _engine_logits(eng, [0, 1])
+        want = o.forward(tok, [0, 3], [0, 1])
+        assert np.array_equal(got[0].view(np.uint32), got[1].view(np.uint32))  # the import decodes as the source
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), step
+
+
 def test_needle3_engine_limits(needle3):
     from needle_cs_b200._native import NeedleError
 
@@ -113,7 +156,7 @@ def test_needle3_engine_limits(needle3):
     with pytest.raises(NeedleError) as e:  # rows of one slot must be consecutive
         eng.forward_batch([1, 2, 3], [5, 0, 5], [])
     assert e.value.status == 100
-    for op in (lambda: eng.mark_slot(0), lambda: eng.export_prefix(0), lambda: eng.copy_slot(1, 0)):
+    for op in (lambda: eng.copy_slot(1, 0), lambda: eng.share_prefix(1, 0), lambda: eng.slot_page(0, 0)):
         with pytest.raises(NeedleError) as e:
             op()
         assert e.value.status == 105
