@@ -676,6 +676,16 @@ NDL_API int ndl_sched_destroy(ndl_sched *s);
  * max_new_tokens tokens or the stop token. */
 NDL_API int ndl_sched_submit(ndl_sched *s, int request, const int32_t *prompt, int prompt_len, int max_new_tokens,
                              int stop_token, const uint32_t *mask, int mask_words);
+/* Jump-forward (NeedleSession.GenerateCalls, src/Needle/NeedleSession.cs:
+ * 538-662): `count` tokens the caller's grammar forces after a decoding
+ * request's last pick (its mask allows one id at each), appended to the
+ * request's output without logits.  The next step feeds the pick and the
+ * forced tokens as one run of the request's slot and samples only at the
+ * run's last row; the stream equals feeding them one per step.  Forced
+ * tokens count toward max_new_tokens and end the request at the stop token.
+ * NDL_ERR_INVALID_ARG for a request that is not decoding or a token outside
+ * the vocabulary. */
+NDL_API int ndl_sched_force(ndl_sched *s, int request, const int32_t *tokens, int count);
 /* Runs one step (none if nothing is queued or running): events of this step
  * (at most `capacity` written, *count = all), rows and decode rows packed. */
 NDL_API int ndl_sched_step(ndl_sched *s, ndl_sched_event *events, int capacity, int *count, int *rows,

@@ -123,6 +123,7 @@ SIGNATURES = {
     "ndl_sched_create_dry": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p]),
     "ndl_sched_destroy": (c_int, [c_void_p]),
     "ndl_sched_submit": (c_int, [c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_void_p, c_int]),
+    "ndl_sched_force": (c_int, [c_void_p, c_int, c_void_p, c_int]),
     "ndl_sched_step": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_void_p]),
     "ndl_sched_tokens": (c_int, [c_void_p, c_int, c_void_p, c_int, c_void_p]),
     "ndl_sched_pending": (c_int, [c_void_p, c_void_p, c_void_p]),

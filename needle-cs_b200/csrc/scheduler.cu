@@ -13,6 +13,14 @@
 // rows.  Because a row's logits do not depend on the rest of the batch, a
 // request's token stream is the one it would get alone.
 //
+// Jump-forward (NeedleSession.GenerateCalls, src/Needle/NeedleSession.cs:
+// 538-662): tokens the caller's grammar forces (the mask allows one id) are
+// appended to a decoding request's output without logits; the next step feeds
+// the request's unfed tokens (its last pick and the forced ones) as one run
+// and samples only at the run's last row, as the reference feeds its call
+// chunk.  A run equals feeding the tokens one per step, so the stream does
+// not change, only the number of forwards.
+//
 // Host code only; single-threaded like the engine (one host thread per
 // engine).  A scheduler made by ndl_sched_create_dry has no engine: it plans
 // steps and "samples" token (request * 7919 + produced) % vocab, which lets
@@ -36,6 +44,8 @@ struct Request {
     std::vector<uint32_t> mask;  // empty: unmasked
     int max_new = 0, stop = -1;
     int slot = -1, fed = 0;
+    int unfed = 0;          // tokens at the end of `out` not yet fed (the last pick and forced tokens)
+    bool finished = false;  // forced tokens reached max_new or the stop token: ends at the next step
     State state = State::Waiting;
     int status = NDL_OK;
     std::vector<int32_t> out;
@@ -178,6 +188,29 @@ NDL_API int ndl_sched_submit(ndl_sched *s, int request, const int32_t *prompt, i
     return NDL_OK;
 }
 
+// Jump-forward: `count` tokens the caller's grammar forces after the
+// request's last pick, appended to its output without sampling; the next
+// step feeds them with that pick as one run (see the file comment).  The
+// request must be decoding; reaching max_new_tokens or the stop token among
+// them ends it at the next step.
+NDL_API int ndl_sched_force(ndl_sched *s, int request, const int32_t *tokens, int count) {
+    NDL_REQUIRE(s && tokens, "null argument");
+    NDL_REQUIRE(count >= 1, "count %d", count);
+    auto it = s->requests.find(request);
+    NDL_REQUIRE(it != s->requests.end(), "request %d was not submitted", request);
+    Request &r = it->second;
+    NDL_REQUIRE(r.state == State::Decode && !r.finished, "request %d is not decoding", request);
+    for (int i = 0; i < count; i++)
+        NDL_REQUIRE(tokens[i] >= 0 && tokens[i] < s->vocab, "forced token %d = %d outside the vocabulary", i,
+                    tokens[i]);
+    for (int i = 0; i < count && !r.finished; i++) {
+        r.out.push_back(tokens[i]);
+        r.unfed++;
+        if ((int)r.out.size() >= r.max_new || tokens[i] == r.stop) r.finished = true;
+    }
+    return NDL_OK;
+}
+
 // One step.  Events: kind 1 = first token (token = its id), kind 2 = the
 // request finished (status 0, or a FailureReason such as 3 ContextExhausted;
 // token = the last id or -1).  *count is the number of events (those beyond
@@ -194,23 +227,37 @@ NDL_API int ndl_sched_step(ndl_sched *s, ndl_sched_event *events, int capacity, 
     s->head_request.clear();
     const int budget = s->cfg.max_rows;
     int n_decode = 0;
-    // decode rows first, in admission order
+    // decode rows first, in admission order: each request's unfed tokens (one,
+    // or a jump-forward run), the logits at the last
     for (int id : s->admitted) {
         Request &r = s->requests[id];
-        if (r.state != State::Decode || (int)s->tokens.size() >= budget) continue;
+        if (r.state != State::Decode) continue;
+        if (r.finished) {
+            push_event(events, capacity, count, id, 2, r.out.back(), r.status);
+            if ((st = release(s, r)) != NDL_OK) return st;
+            continue;
+        }
+        const int n = std::min(r.unfed, budget - (int)s->tokens.size());
+        if (n <= 0) continue;
         int len = 0;
         if ((st = slot_length(s, r.slot, &len)) != NDL_OK) return st;
-        if (len + 1 > s->capacity) {
+        if (len + n > s->capacity) {
             r.status = NDL_FAIL_CONTEXT_EXHAUSTED;
             push_event(events, capacity, count, id, 2, r.out.empty() ? -1 : r.out.back(), r.status);
             if ((st = release(s, r)) != NDL_OK) return st;
             continue;
         }
-        s->head_rows.push_back((int)s->tokens.size());
-        s->head_request.push_back(id);
-        s->tokens.push_back(r.out.back());
-        s->row_slots.push_back(r.slot);
-        n_decode++;
+        const int first = (int)r.out.size() - r.unfed;
+        for (int i = 0; i < n; i++) {
+            s->tokens.push_back(r.out[first + i]);
+            s->row_slots.push_back(r.slot);
+        }
+        r.unfed -= n;
+        if (r.unfed == 0) {  // the run is complete: its last row samples the next token
+            s->head_rows.push_back((int)s->tokens.size() - 1);
+            s->head_request.push_back(id);
+        }
+        n_decode += n;
     }
     // then prompt chunks
     for (int id : s->admitted) {
@@ -267,6 +314,7 @@ NDL_API int ndl_sched_step(ndl_sched *s, ndl_sched_event *events, int capacity, 
             continue;
         }
         r.out.push_back(tok);
+        r.unfed = 1;
         if (r.state == State::Prefill) {
             r.state = State::Decode;
             push_event(events, capacity, count, r.id, 1, tok, NDL_OK);

@@ -54,6 +54,12 @@ class Scheduler:
             call("ndl_sched_submit", self._h, request, p.ctypes.data, p.size, max_new_tokens, stop_token,
                  m.ctypes.data, m.size)
 
+    def force(self, request, tokens):
+        """Jump-forward: grammar-forced tokens after the request's last pick
+        (ndl_sched_force); the next step feeds them as one run."""
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        call("ndl_sched_force", self._h, request, t.ctypes.data, t.size)
+
     def step(self):
         """One step: (events [(request, kind, token, status)], rows, decode_rows)."""
         n, rows, dec = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()

@@ -112,3 +112,45 @@ def test_rejects_bad_requests(sched_mod):
     s.submit(0, [1], 1)
     with pytest.raises(NeedleError):
         s.submit(0, [1], 1)                   # duplicate id
+
+
+def test_jump_forward_runs(sched_mod):
+    """Forced tokens (NeedleSession.GenerateCalls' jump-forward,
+    src/Needle/NeedleSession.cs:538-662) join the request's output without a
+    sample; the next step feeds the last pick and the forced tokens as one
+    contiguous run of the request's slot with the head at its last row; they
+    count toward max_new_tokens, and a stop token among them ends the request."""
+    from needle_cs_b200._native import NeedleError
+
+    vocab = 1000
+    s = sched_mod.Scheduler(None, max_rows=8, prefill_chunk=8, slots=2, capacity=64, vocab=vocab)
+    s.submit(0, np.arange(3, dtype=np.int32), 12)
+    s.submit(1, np.arange(5, dtype=np.int32), 6, stop_token=77)
+    with pytest.raises(NeedleError):  # not decoding yet
+        s.force(0, [5])
+    s.step()  # both prompts, first tokens
+    s.step()  # one decode row each
+    out0 = list(s.tokens(0))
+    assert len(out0) == 2
+    s.force(0, [501, 502, 503])
+    ev, rows, dec = s.step()
+    tokens, row_slots, heads = s.last_plan()
+    r0 = [i for i, sl in enumerate(row_slots) if sl == row_slots[0]]
+    assert [int(tokens[i]) for i in r0] == [out0[-1], 501, 502, 503]  # the pick, then the forced run
+    assert r0 == list(range(r0[0], r0[0] + 4)) and r0[-1] in list(heads)
+    assert list(s.tokens(0))[:5] == out0 + [501, 502, 503]
+    assert len(s.tokens(0)) == 6  # and the run's sample
+    # a run longer than the step's free rows is split; the head waits for its last row
+    s.force(0, list(range(600, 612))[:5])
+    ev, rows, dec = s.step()
+    assert rows <= 8
+    # the stop token among forced tokens ends request 1 at the next step
+    s.force(1, [5, 77])
+    ev, rows, dec = s.step()
+    finished = [e for e in ev if e[0] == 1 and e[1] == sched_mod.FINISHED]
+    assert finished and finished[0][2] == 77
+    assert list(s.tokens(1))[-2:] == [5, 77]
+    with pytest.raises(NeedleError):
+        s.force(1, [5])  # done
+    with pytest.raises(NeedleError):
+        s.force(0, [vocab])  # outside the vocabulary
