@@ -28,10 +28,10 @@ LINEAR_METRIC = "int8 linear GB/s (algorithmic bytes)"
 FALLBACK_HBM_GBS = 6650.0
 # DRAM bytes (read + write) per algorithmic byte of attn_decode_kernel, from a
 # full ncu capture of the cfg5 launch shape on a 2-layer engine
-# (needle-cs_b200/profile_case.py attention: 320.8 MB for 298.2 MB); the
+# (python bench.py --case attention: 319.9 MB for 298.2 MB); the
 # excess is the unused tail of each row's last 64-position page, so traffic
 # grows with the algorithmic bytes and scales to the 12-layer launch.
-ATTN_TRAFFIC_PER_ALG_BYTE = 1.076
+ATTN_TRAFFIC_PER_ALG_BYTE = 1.073
 
 
 def host_cpu():
