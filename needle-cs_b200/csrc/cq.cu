@@ -126,13 +126,18 @@ __device__ __forceinline__ uint32_t cq_nibble_sel(uint32_t w) {
     const uint32_t u = (kHigh ? w >> 4 : w) & 0x0F0F0F0Fu;  // nibble of byte k at bits 8k..8k+3
     return cq_prmt(u | (u >> 4), 0u, 0x0020u);            // bytes 0 and 2 hold nibbles (0, 1) and (2, 3)
 }
-// Codebook bytes of the four 2-bit indices of plane kS (bits 2kS..2kS+1 of
-// each byte): a nibble holds planes (0, 1) or (2, 3), so one selector serves
-// two planes, the low one through an index masked to 2 bits, the high one
-// shifted down.
-template <int kS>
-__device__ __forceinline__ uint32_t cq_lut2_sel(uint32_t sel, uint32_t t0) {
-    return (kS & 1) ? cq_prmt(t0, 0u, (sel >> 2) & 0x3333u) : cq_prmt(t0, 0u, sel & 0x3333u);
+// The codebook bytes of a word's sixteen 2-bit indices (index m at bits
+// 2m..2m+1: byte m >> 2, plane m & 3) in four permutes, o[k] for MMA k:
+// o[0] = indices 0, 2, 4, 6; o[1] = 1, 3, 5, 7; o[2] = 8, 10, 12, 14;
+// o[3] = 9, 11, 13, 15.  A prmt selector nibble (bits 4n..4n+3 of the
+// shifted word) holds two indices; with the top bit cleared its low three
+// bits pick a byte of (t0, t0), the 4-entry book twice, so the nibble's
+// second index drops out.  Eleven integer operations for 16 indices.
+__device__ __forceinline__ void cq_decode2(uint32_t w, uint32_t t0, uint32_t (&o)[4]) {
+    o[0] = cq_prmt(t0, t0, w & 0x7777u);
+    o[1] = cq_prmt(t0, t0, (w >> 2) & 0x7777u);
+    o[2] = cq_prmt(t0, t0, (w >> 16) & 0x7777u);
+    o[3] = cq_prmt(t0, t0, (w >> 18) & 0x7777u);
 }
 
 // Codebook bytes for the four 4-bit indices in the low (kS = 0) or high
@@ -164,9 +169,10 @@ __device__ __forceinline__ void cq_mma(int (&d)[4], const uint32_t (&a)[4], uint
 // mma.sync m16n8k32 s8 (byte permutes in registers), the prepared
 // activations the B fragment (shared memory, rows padded by 16 bytes so the
 // fragment loads hit 32 distinct banks); the four chunks chain in the
-// accumulator to the exact group dot.  Chunk k of a group is plane k
-// (2-bit: bits 2k..2k+1 of bytes 0..31) or nibble k&1 of bytes 32(k>>1)..+31
-// (4-bit), matching the plane order Prepare writes.  Each lane then folds
+// accumulator to the exact group dot.  4-bit: chunk k of a group is nibble
+// k&1 of bytes 32(k>>1)..+31, the plane order Prepare writes; 2-bit: the
+// decode's own order (cq_decode2), the activations permuted to match when
+// they are staged.  Each lane then folds
 // its four (row, token) dots per column block into fp32 in ascending group
 // order.
 template <int kBits>
@@ -182,11 +188,31 @@ __global__ void __launch_bounds__(32 * kCqWarps, 2) cq_matmul_kernel(
     float *ss = reinterpret_cast<float *>(smem + (size_t)kCqMaxTokens * xstride);    // [16][groups]
     float *os = ss + kCqMaxTokens * groups;
     pdl_enter();
-    for (int i = threadIdx.x; i < kCqMaxTokens * (cols / 16); i += blockDim.x) {
-        const int t = i / (cols / 16), c = i - t * (cols / 16);
-        const uint4 v = t < tokens ? reinterpret_cast<const uint4 *>(values + (size_t)t * cols)[c]
-                                   : make_uint4(0u, 0u, 0u, 0u);
-        *reinterpret_cast<uint4 *>(xs + (size_t)t * xstride + 16 * c) = v;
+    if (kBits == 2) {
+        // the activations in the order the 2-bit decode produces codes (see cq_decode2): slot s of MMA k in
+        // a group holds plane p(k, i) of byte 16 * half + 4 * tig + b(k, i), with s = 16 * half + 4 * tig + i,
+        // b = 2 (k >> 1) + (i >> 1), p = (k & 1) + 2 (i & 1); the group dot is an exact int32 sum in any order
+        for (int i = threadIdx.x; i < kCqMaxTokens * (cols / 4); i += blockDim.x) {
+            const int t = i / (cols / 4), ow = i - t * (cols / 4), g = ow >> 5, s0 = 4 * (ow & 31);
+            const int k = s0 >> 5, half = (s0 >> 4) & 1, tg = (s0 >> 2) & 3;
+            uint32_t out = 0u;
+            if (t < tokens) {
+                const int8_t *src = values + (size_t)t * cols + (size_t)g * 128 + half * 16 + tg * 4;
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    const int b = 2 * (k >> 1) + (j >> 1), p = (k & 1) + 2 * (j & 1);
+                    out |= (uint32_t)(uint8_t)src[p * 32 + b] << (8 * j);
+                }
+            }
+            *reinterpret_cast<uint32_t *>(xs + (size_t)t * xstride + 4 * ow) = out;
+        }
+    } else {
+        for (int i = threadIdx.x; i < kCqMaxTokens * (cols / 16); i += blockDim.x) {
+            const int t = i / (cols / 16), c = i - t * (cols / 16);
+            const uint4 v = t < tokens ? reinterpret_cast<const uint4 *>(values + (size_t)t * cols)[c]
+                                       : make_uint4(0u, 0u, 0u, 0u);
+            *reinterpret_cast<uint4 *>(xs + (size_t)t * xstride + 16 * c) = v;
+        }
     }
     for (int i = threadIdx.x; i < kCqMaxTokens * groups; i += blockDim.x) {
         const int t = i / groups, g = i - t * groups;
@@ -254,23 +280,22 @@ __global__ void __launch_bounds__(32 * kCqWarps, 2) cq_matmul_kernel(
                     for (int nt = 0; nt < 2; nt++)
 #pragma unroll
                         for (int i = 0; i < 4; i++) d[nt][i] = 0;
-                    // 2-bit: nibble selectors of the four index words (a0..a3 order), planes (0, 1) and (2, 3)
-                    uint32_t sel_lo[4], sel_hi[4];
+                    // 2-bit: the codebook bytes of the four index words (a0..a3 order), four MMAs' worth each
+                    uint32_t dec[4][4];
                     if (kBits == 2) {
                         const uint32_t wds[4] = {c0[tt][cg][0][0], c1[tt][cg][0][0], c0[tt][cg][0][1], c1[tt][cg][0][1]};
 #pragma unroll
-                        for (int j = 0; j < 4; j++) sel_lo[j] = cq_nibble_sel<0>(wds[j]), sel_hi[j] = cq_nibble_sel<1>(wds[j]);
+                        for (int j = 0; j < 4; j++) cq_decode2(wds[j], book.bytes[0], dec[j]);
                     }
 #pragma unroll
                     for (int k = 0; k < 4; k++) {
                         const int h = kBits == 2 ? 0 : k >> 1;
                         uint32_t a[4];
                         if (kBits == 2) {
-                            const uint32_t *sel = k < 2 ? sel_lo : sel_hi;
-                            a[0] = (k & 1) ? cq_lut2_sel<1>(sel[0], book.bytes[0]) : cq_lut2_sel<0>(sel[0], book.bytes[0]);
-                            a[1] = (k & 1) ? cq_lut2_sel<1>(sel[1], book.bytes[0]) : cq_lut2_sel<0>(sel[1], book.bytes[0]);
-                            a[2] = (k & 1) ? cq_lut2_sel<1>(sel[2], book.bytes[0]) : cq_lut2_sel<0>(sel[2], book.bytes[0]);
-                            a[3] = (k & 1) ? cq_lut2_sel<1>(sel[3], book.bytes[0]) : cq_lut2_sel<0>(sel[3], book.bytes[0]);
+                            a[0] = dec[0][k];
+                            a[1] = dec[1][k];
+                            a[2] = dec[2][k];
+                            a[3] = dec[3][k];
                         } else {
                             a[0] = cq_lut_plane4(c0[tt][cg][h][0], k & 1, book.bytes);
                             a[1] = cq_lut_plane4(c1[tt][cg][h][0], k & 1, book.bytes);
