@@ -130,7 +130,34 @@ __global__ void __launch_bounds__(256) argmax_masked_kernel(const float *__restr
     const int limit = mr ? min(length, words * 32) : length;
     float best = -INFINITY;
     int best_i = -1;
-    for (int i = threadIdx.x; i < limit; i += blockDim.x) {
+    // each thread scans four consecutive ids at a time (one 16-byte load, ids in increasing order, so the
+    // first of equal values stays), four such loads in flight per pass
+    const bool vec = (ldx & 3) == 0 && (reinterpret_cast<uintptr_t>(xr) & 15) == 0;
+    const int quads = vec ? limit >> 2 : 0;
+    for (int q0 = threadIdx.x; q0 < quads; q0 += 4 * blockDim.x) {
+        float4 v[4];
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const int q = q0 + u * blockDim.x;
+            v[u] = q < quads ? __ldg(reinterpret_cast<const float4 *>(xr) + q) : make_float4(-INFINITY, -INFINITY,
+                                                                                              -INFINITY, -INFINITY);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const int q = q0 + u * blockDim.x;
+            if (q >= quads) break;
+            const uint32_t bits = mr ? (mr[q >> 3] >> ((q & 7) * 4)) & 0xFu : 0xFu;
+            const float e[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+#pragma unroll
+            for (int j = 0; j < 4; j++)
+                if (((bits >> j) & 1u) && e[j] > best) {
+                    best = e[j];
+                    best_i = 4 * q + j;
+                }
+        }
+    }
+    // the scalar remainder (and every id when the row cannot be read as float4)
+    for (int i = 4 * quads + threadIdx.x; i < limit; i += blockDim.x) {
         if (mr && !((mr[i >> 5] >> (i & 31)) & 1u)) continue;
         const float v = xr[i];
         if (v > best) {
