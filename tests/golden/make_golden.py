@@ -1,9 +1,8 @@
 """Regenerate tests/golden/conformance_golden.json from the reference sources.
 
-Run in a container where the needle-cs source tree is mounted (default
-location below, or pass its path as the first argument):
+Run where a needle-cs source tree is available, passing its path:
 
-    python tests/golden/make_golden.py [NEEDLE_CS_ROOT]
+    python tests/golden/make_golden.py NEEDLE_CS_ROOT
 
 Two sources feed the fixture:
   * "fixtures": the golden math truths printed by the reference's own
