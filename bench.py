@@ -1034,6 +1034,125 @@ def run_prefix(args, rank, world, local):
 #  gemm M N K: five calls of the I8G32 linear on random int8 activations and
 #    weights with fp16 group scales (M >= 64: the tcgen05 GEMM, else the GEMV).
 
+NEEDLE3_SHAPE = dict(dim=768, heads=12, kv_heads=2, layers=20, vocab=8192, hada_n=1024, engram_tables=6,
+                     engram_sub=128, engram_seed_heads=3, orders=[2, 3], sites=[1, 10], sliding_window=256,
+                     global_mask=sum(1 << l for l in range(3, 20, 4)), max_seq=512)
+
+
+def needle3_archive(seed):
+    """A synthetic archive of Needle 3's shape (20 layers, d 768, 12 query heads over 2 kv heads of 48 / 64
+    dims, vocab 8192, the Kronecker MLP over HadaN 1024, Engram sites at layers 1 and 10; CQ weights with
+    random codes), written by the test suite's archive writer."""
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    from cact_support import needle3_decoder_archive
+
+    return needle3_decoder_archive(seed=seed, **NEEDLE3_SHAPE)
+
+
+def run_needle3(args, rank, world, local):
+    """The Needle-3 decoder through ndl_forward_batch (ndl_engine_create_model) on a synthetic archive of
+    Needle 3's shape.  64 sessions per GPU (the reference's ForwardBatch row cap) each prefill a 32-token
+    prompt, one row per session per forward; then every step decodes one row per session, greedy.
+    value = tokens per second over the timed steps (CUDA events around them, max over ranks); e2e = the
+    same on the host clock with every step's tokens sent and ids read back through the public API.  The
+    roofline line is the step against HBM: the weights it reads (CQ codes and norms, dense tensors) plus
+    each session's K / V cache, per step over the step's time."""
+    import torch
+
+    pkg = entry.load_package()
+    pkg.lib()
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    cact = __import__("needle_cs_b200.model", fromlist=["model"])
+    eng_mod = __import__("needle_cs_b200.engine", fromlist=["engine"])
+    a = needle3_archive(seed=5)
+    data = a.build()
+    m = cact.Model(data, device=local)
+    g = m.info
+    B, P = 64, 32
+    cap = P + args.warmup + args.steps + 8
+    eng = eng_mod.BatchedEngine.from_model(m, slots=B, context_length=cap, chunk_size=B, max_heads=B)
+    rng = np.random.default_rng(rank)
+    slots = np.arange(B, dtype=np.int32)
+    heads = np.arange(B, dtype=np.int32)
+    prompt = rng.integers(0, g["vocab"], (B, P)).astype(np.int32)
+    for i in range(P):
+        eng.forward_batch(prompt[:, i], slots, heads if i == P - 1 else [])
+    ids = eng.sample_argmax()
+    for _ in range(args.warmup):
+        eng.forward_batch(ids, slots, heads)
+        ids = eng.sample_argmax()
+    eng.sync()
+    stream = torch.cuda.ExternalStream(eng.stream())
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    with ClockSampler(torch.cuda.get_device_properties(device).uuid) as clocks:
+        t0 = time.perf_counter()
+        e0.record(stream)
+        for _ in range(args.steps):
+            eng.forward_batch(ids, slots, heads)
+            ids = eng.sample_argmax()
+        e1.record(stream)
+        eng.sync()
+        wall = time.perf_counter() - t0
+    ms = max_over_ranks(e0.elapsed_time(e1), world)
+    wall = max_over_ranks(wall * 1e3, world) * 1e-3
+    value = world * B * args.steps / (ms * 1e-3)
+    d, L = g["dim"], g["layers"]
+    kw, vw = g["kv_heads"] * g["qk_dim"], g["kv_heads"] * g["v_dim"]
+    weights = sum(len(r[4]) for r in a.records if r[0] != "tokenizer" and not r[0].startswith("probe."))
+    mean_len = P + args.warmup + args.steps / 2 + 1
+    kv_bytes = B * mean_len * L * (kw + vw + 8 * g["kv_heads"])
+    step_bytes = weights + kv_bytes
+    achieved = step_bytes / (ms * 1e-3 / args.steps) / 1e9
+    peak, peak_source = hbm_peak()
+    line = {"metric": "needle3 decode tokens/sec/box", "value": value, "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "u2/u4 codes x int8 -> int32, f32",
+            "data": "synthetic", "config": {"workload": "needle3_decode", "model": "synthetic archive of Needle 3's "
+                                            "shape", "geometry": {k: g[k] for k in ("layers", "dim", "heads", "kv_heads",
+                                                                                    "qk_dim", "v_dim", "vocab", "hada_n",
+                                                                                    "sliding_window")},
+                                            "sites": list(g["sites"][:g["site_count"]]), "sessions_per_gpu": B,
+                                            "prompt": P, "greedy": True, "weight_bytes": weights,
+                                            "l2": "weights fit L2; each step reads them and every session's cache"},
+            "roofline": {"bound": "hbm", "kernel": "the whole step (launch- and latency-bound: ~27 kernels per layer "
+                                                   "on 64 rows, replayed from a CUDA graph)",
+                         "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak, "traffic": None,
+                         "peak_source": peak_source, "algorithmic_bytes_per_step": step_bytes},
+            "e2e": {"value": world * B * args.steps / wall, "unit": "tokens/s", "h2d_bytes_per_step": B * 12,
+                    "d2h_bytes_per_step": B * 4},
+            "gpu_launches": args.steps * (L * 27 + 8), "clocks": clocks.summary()}
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        entry.load_oracle()
+        line["cpu_baseline"] = needle3_cpu_sample(a)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    eng.close()
+    m.close()
+
+
+def needle3_cpu_sample(a, steps=2):
+    """The CPU restatement of the same Needle-3 step (oracle/needle3.py, the scalar tier, one thread), built
+    from the archive alone: 4 sessions prefill 8 tokens, then `steps` decode steps of 4 rows are timed."""
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    from needle3_support import oracle_from_archive
+
+    o = oracle_from_archive(a, 4, 64)
+    rng = np.random.default_rng(0)
+    slots = [0, 1, 2, 3]
+    vocab = a.g["vocab"]
+    for _ in range(8):
+        o.forward(rng.integers(0, vocab, 4), slots, [])
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        o.forward(rng.integers(0, vocab, 4), slots, [0, 1, 2, 3])
+    dt = time.perf_counter() - t0
+    return {"value": 4 * steps / dt, "unit": "tokens/s", "cores": 1, "kind": "port",
+            "sample": f"{steps} decode steps of 4 sessions after an 8-token prefill, the scalar-tier chain "
+                      f"(oracle/needle3.py over oracle/needle_oracle.c), 1 thread; {host_cpu()[0]}"}
+
+
 def case_attention(steps=4, rows=512, seed=5):
     entry.load_package()
     from needle_cs_b200.engine import BatchedEngine, SyntheticDecoder
@@ -1076,7 +1195,7 @@ def case_gemm(m, n, k, calls=5):
 
 
 WORKLOADS = {"cfg1": GemvWorkload, "cfg2": DecodeWorkload, "cfg3": ServingWorkload, "cfg4": BeamWorkload,
-             "cfg5": DecodeWorkload, "prefix": None, "cq": CqWorkload}
+             "cfg5": DecodeWorkload, "prefix": None, "cq": CqWorkload, "needle3": None}
 DECODE = ("cfg2", "cfg5")
 
 
@@ -1094,6 +1213,16 @@ def run_reference(args, rank, world):
     if rank != 0:
         return
     oracle = entry.load_oracle()
+    if args.workload == "needle3":
+        base = needle3_cpu_sample(needle3_archive(seed=5), steps=max(2, min(args.steps, 4)))
+        print(json.dumps({"impl": "reference", "metric": "needle3 decode tokens/sec/box", "value": base["value"],
+                          "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+                          "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                          "dtype": "u2/u4 codes x int8 -> int32, f32", "data": "synthetic",
+                          "config": {"workload": "needle3_decode"}, "cpu_baseline": base,
+                          "e2e": {"value": base["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                                  "d2h_bytes_per_step": 0}}), flush=True)
+        return
     wl = make_workload(args.workload, args)
     if args.workload == "cfg3":
         entry.load_package()
@@ -1366,6 +1495,8 @@ def main():
             run_beam(args, rank, world, local)
         elif args.workload == "prefix":
             run_prefix(args, rank, world, local)
+        elif args.workload == "needle3":
+            run_needle3(args, rank, world, local)
         else:
             run_ours(args, rank, world, local)
     finally:

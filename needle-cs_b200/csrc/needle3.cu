@@ -92,6 +92,12 @@ struct N3State {
     float *snap_conv = nullptr, *snap_ehist = nullptr;
     int32_t *snap_prev = nullptr;
     int pool_rows = 0;  // the confidence head's pool rows the reference's state carries (this engine does not pool)
+    // captured single-wave forwards (every row a distinct slot, head rows in order), keyed by (rows, heads)
+    struct WaveGraph {
+        int rows, heads;
+        cudaGraphExec_t exec;
+    };
+    std::vector<WaveGraph> graphs;
 };
 
 namespace {
@@ -537,6 +543,37 @@ int forward_wave(N3State *s, const int32_t *tokens, const int32_t *slots, const 
 
 }  // namespace
 
+// A single-wave forward (rows of distinct slots, staged at d_rows) replayed
+// from a CUDA graph per (rows, heads); the first call of a shape captures it.
+static int launch_wave_graph(N3State *s, int rows, int heads, float *logits, cudaStream_t st) {
+    for (auto &g : s->graphs)
+        if (g.rows == rows && g.heads == heads) {
+            NDL_CUDA(cudaGraphLaunch(g.exec, st));
+            return NDL_OK;
+        }
+    cudaGraph_t graph = nullptr;
+    NDL_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+    int rc = forward_wave(s, s->d_rows, s->d_rows + rows, s->d_rows + 2 * rows, rows, heads, logits, st);
+    cudaError_t end = cudaStreamEndCapture(st, &graph);
+    if (rc != NDL_OK || end != cudaSuccess) {
+        if (graph) cudaGraphDestroy(graph);
+        cudaGetLastError();
+        if (rc != NDL_OK) return rc;
+        return set_error(NDL_ERR_CUDA, "Needle-3 step capture: %s", cudaGetErrorString(end));
+    }
+    cudaGraphExec_t exec = nullptr;
+    cudaError_t inst = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (inst != cudaSuccess) return set_error(NDL_ERR_CUDA, "Needle-3 step graph: %s", cudaGetErrorString(inst));
+    if (s->graphs.size() >= 16) {  // keep the 16 latest shapes
+        cudaGraphExecDestroy(s->graphs.front().exec);
+        s->graphs.erase(s->graphs.begin());
+    }
+    s->graphs.push_back({rows, heads, exec});
+    NDL_CUDA(cudaGraphLaunch(exec, st));
+    return NDL_OK;
+}
+
 // ForwardBatch over rows whose runs (consecutive rows of one slot) become
 // waves: wave w holds the w-th row of every run, so each wave's rows are
 // distinct slots and a run's rows go in order.  All waves' rows are staged
@@ -588,6 +625,14 @@ int n3_forward(N3State *s, cudaStream_t st, const int *tokens, const int *row_sl
     }
     hstart[waves] = hat;
     NDL_CUDA(cudaMemcpyAsync(s->d_rows, h, (size_t)(2 * rows + heads) * sizeof(int32_t), cudaMemcpyHostToDevice, st));
+    bool in_order = waves == 1;
+    for (int k = 0; k < heads && in_order; k++) in_order = head_dst[k] == k;
+    if (in_order) {  // a decode step: one wave, the logits straight into place, from a captured graph
+        N3_TRY(launch_wave_graph(s, rows, heads, logits, st));
+        for (int r = 0; r < rows; r++) s->host_len[row_slots[r]]++;
+        NDL_CUDA(cudaStreamSynchronize(st));
+        return NDL_OK;
+    }
     for (int w = 0; w < waves; w++) {
         const int n = start[w + 1] - start[w], nh = hstart[w + 1] - hstart[w];
         N3_TRY(forward_wave(s, s->d_rows + start[w], s->d_rows + rows + start[w], s->d_rows + 2 * rows + hstart[w], n,
@@ -886,6 +931,7 @@ int n3_create(const ndl_model *m, int slots, int capacity, int max_rows, int max
 
 void n3_destroy(N3State *s) {
     if (!s) return;
+    for (auto &g : s->graphs) cudaGraphExecDestroy(g.exec);
     for (void *p : s->allocations) cudaFree(p);
     if (s->h_rows) cudaFreeHost(s->h_rows);
     delete s;

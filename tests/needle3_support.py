@@ -25,3 +25,30 @@ def oracle_for(archive, model, slots, capacity):
         return np.ascontiguousarray(model.host(role, 0), np.int32)
 
     return Needle3Oracle(model.info, archive.levels, dense, cq, perm, slots, capacity)
+
+
+def oracle_from_archive(archive, slots, capacity):
+    """The same oracle built from the archive writer's records alone (no
+    library): dense fp16 tensors by Scalar.HalfToSingle, the geometry as the
+    loader derives it."""
+    from cact_support import half_to_single
+    from oracle.needle3 import Needle3Oracle
+
+    g = archive.g
+    rec = {(r[0], r[1]): r[6] for r in archive.records}
+    rows = 1 << ((g["hada_n"] - 1).bit_length() // 2)
+    info = dict(g, hada_rows=rows, hada_cols=g["hada_n"] // rows, order_count=len(g["orders"]),
+                site_count=len(g["sites"]), vocab=g["vocab"])
+
+    def cq(role, index):
+        _, codes, norms, nrows, cols, bits = rec[(role, index)]
+        return codes.reshape(nrows, -1), norms.reshape(nrows, -1), nrows, cols, bits
+
+    def dense(role, index=0):
+        kind, v = rec[(role, index)][:2]
+        return half_to_single(v, exact=True) if kind == "dense16" else np.ascontiguousarray(v, np.float32)
+
+    def perm(role):
+        return np.ascontiguousarray(rec[(role, 0)][1], np.int32)
+
+    return Needle3Oracle(info, archive.levels, dense, cq, perm, slots, capacity)
