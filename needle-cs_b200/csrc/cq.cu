@@ -23,6 +23,8 @@ constexpr float kCqHadamardScale = 0.08838834764831845f;  // Scalar.cs:49 (Quant
 constexpr int kCqMaxTokens = 16;                          // tokens per matmul launch (lane t folds token t)
 constexpr int kCqWarps = 8;
 constexpr int kCqMaxCols = 8192;
+constexpr int kCqSplitWarps = 4;  // warps per CTA of cq_matmul_split_kernel (they split the groups)
+constexpr int kCqMaxJobs = 4;     // matrices per cq_matmul_split_kernel launch
 
 __device__ __forceinline__ int8_t cq_quant1(float x, float inverse) {
     const float r = rintf(__fmul_rn(x, inverse));
@@ -337,6 +339,125 @@ __global__ void __launch_bounds__(32 * kCqWarps, 2) cq_matmul_kernel(
     }
 }
 
+// Up to kCqMaxJobs matrices over the same prepared activations in one launch
+// (the projections of one layer); jobs in ascending tile_begin order.
+struct CqJob {
+    const uint32_t *indices;
+    const uint16_t *norms;
+    float *y;
+    CqBook book;
+    int ldy, row_start, row_end, tile_begin;
+};
+struct CqJobList {
+    CqJob job[kCqMaxJobs];
+    int n;
+};
+
+// The same MatMulRows for many tokens or few rows: CTA per (job, 16-row
+// tile, 8-token block).  Its warps split the 128-column groups (warp w takes
+// groups w, w + kCqSplitWarps, ...): per group the A fragments as in
+// cq_matmul_kernel, the B fragments loaded straight from the prepared values
+// (each lane's eight words g*128 + 4*tig + 16*j of its token; for 2-bit the
+// plane permutation of cq_matmul_kernel's staging done with byte permutes),
+// four mma.sync, and the exact int32 dots left in shared memory with the
+// rows' norm * byte_scale and the tokens' scales and offsets.  Then thread
+// (row, token) folds the groups in ascending order with the same fp32 steps
+// as cq_matmul_kernel (Scalar.MatMulRows, src/Needle/Scalar.cs:146-192).
+template <int kBits>
+__global__ void __launch_bounds__(32 * kCqSplitWarps) cq_matmul_split_kernel(
+    CqJobList jobs, int cols, const int8_t *__restrict__ values, const float *__restrict__ scales,
+    const float *__restrict__ offsets, int stride, int tokens) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    const int groups = cols / 128, row_words = cols * kBits / 32;
+    constexpr int kGroupWords = kBits == 2 ? 8 : 16;
+    constexpr int kBlocks = kBits == 2 ? 1 : 2;
+    const int token_blocks = (tokens + 7) >> 3;
+    const int tile = blockIdx.x / token_blocks, tb = blockIdx.x - tile * token_blocks;
+    CqJob job = jobs.job[0];
+#pragma unroll
+    for (int i = 1; i < kCqMaxJobs; i++)
+        if (i < jobs.n && tile >= jobs.job[i].tile_begin) job = jobs.job[i];
+    const int r_base = job.row_start + (tile - job.tile_begin) * 16;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
+    int *dots = reinterpret_cast<int *>(smem);                   // [groups][16 rows][8 tokens]
+    float *nf = reinterpret_cast<float *>(dots + groups * 128);  // [groups][16]
+    float *ss = nf + groups * 16;                                // [groups][8]
+    float *os = ss + groups * 8;                                 // [groups][8]
+    const int r0 = r_base + gid, r1 = r0 + 8, t = tb * 8 + gid;
+    const bool ok0 = r0 < job.row_end, ok1 = r1 < job.row_end, okt = t < tokens;
+    const uint32_t *w0 = job.indices + (size_t)(ok0 ? r0 : job.row_start) * row_words;
+    const uint32_t *w1 = job.indices + (size_t)(ok1 ? r1 : job.row_start) * row_words;
+    const uint32_t *xw = reinterpret_cast<const uint32_t *>(values + (size_t)(okt ? t : 0) * cols) + tig;
+    // one side value per lane and group: lanes 0..15 a row's norm * byte_scale,
+    // 16..23 a token's scale, 24..31 its offset
+    const int side_row = r_base + (lane & 15), side_tok = tb * 8 + (lane & 7);
+    const bool side_ok = lane < 16 ? side_row < job.row_end : side_tok < tokens;
+    const float *side_src = lane < 24 ? scales : offsets;
+    float *side_dst = lane < 16 ? nf + lane : lane < 24 ? ss + (lane - 16) : os + (lane - 24);
+    const int side_step = lane < 16 ? 16 : 8;
+    pdl_enter();
+#pragma unroll 2
+    for (int g = warp; g < groups; g += kCqSplitWarps) {
+        uint32_t c0[kBlocks][2], c1[kBlocks][2], x[8];
+#pragma unroll
+        for (int h = 0; h < kBlocks; h++) {
+            const int wi = g * kGroupWords + 8 * h + tig;
+            c0[h][0] = ok0 ? __ldg(w0 + wi) : 0u;
+            c0[h][1] = ok0 ? __ldg(w0 + wi + 4) : 0u;
+            c1[h][0] = ok1 ? __ldg(w1 + wi) : 0u;
+            c1[h][1] = ok1 ? __ldg(w1 + wi + 4) : 0u;
+        }
+#pragma unroll
+        for (int j = 0; j < 8; j++) x[j] = okt ? __ldg(xw + g * 32 + 4 * j) : 0u;
+        float side = 0.0f;
+        if (side_ok)
+            side = lane < 16 ? __fmul_rn(half_to_float_ref_fast(job.norms[(size_t)side_row * groups + g]),
+                                         job.book.byte_scale)
+                             : side_src[(size_t)side_tok * stride + g];
+        int d[4] = {0, 0, 0, 0};
+        if (kBits == 2) {
+            uint32_t dec[4][4];
+            const uint32_t wds[4] = {c0[0][0], c1[0][0], c0[0][1], c1[0][1]};
+#pragma unroll
+            for (int j = 0; j < 4; j++) cq_decode2(wds[j], job.book.bytes[0], dec[j]);
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                // byte i of half h of MMA k: plane (k & 1) + 2 (i & 1) of byte 2 (k >> 1) + (i >> 1), i.e.
+                // word h + 2 (k & 1) (even i) or h + 2 (k & 1) + 4 (odd i) of this lane's eight
+                const uint32_t a[4] = {dec[0][k], dec[1][k], dec[2][k], dec[3][k]};
+                const uint32_t sel = (k >> 1) ? 0x7362u : 0x5140u;
+                const int p = 2 * (k & 1);
+                cq_mma(d, a, cq_prmt(x[p], x[p + 4], sel), cq_prmt(x[p + 1], x[p + 5], sel));
+            }
+        } else {
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                const int h = k >> 1;
+                const uint32_t a[4] = {cq_lut_plane4(c0[h][0], k & 1, job.book.bytes),
+                                       cq_lut_plane4(c1[h][0], k & 1, job.book.bytes),
+                                       cq_lut_plane4(c0[h][1], k & 1, job.book.bytes),
+                                       cq_lut_plane4(c1[h][1], k & 1, job.book.bytes)};
+                cq_mma(d, a, x[2 * k], x[2 * k + 1]);
+            }
+        }
+        // rows gid, gid + 8; tokens 2 tig, 2 tig + 1
+        *reinterpret_cast<int2 *>(dots + g * 128 + gid * 8 + 2 * tig) = make_int2(d[0], d[1]);
+        *reinterpret_cast<int2 *>(dots + g * 128 + (gid + 8) * 8 + 2 * tig) = make_int2(d[2], d[3]);
+        side_dst[g * side_step] = side;
+    }
+    __syncthreads();
+    if (threadIdx.x >= 128) return;
+    const int r = threadIdx.x >> 3, tk = threadIdx.x & 7;
+    float acc = 0.0f, bias = 0.0f;
+    for (int g = 0; g < groups; g++) {
+        const float scaled = __fmul_rn(nf[g * 16 + r], ss[g * 8 + tk]);
+        acc = __fadd_rn(acc, __fmul_rn(scaled, (float)dots[g * 128 + r * 8 + tk]));
+        bias = __fadd_rn(bias, __fmul_rn(scaled, os[g * 8 + tk]));
+    }
+    const int row = r_base + r, tok = tb * 8 + tk;
+    if (row < job.row_end && tok < tokens) job.y[(size_t)tok * job.ldy + row] = __fsub_rn(acc, bias);
+}
+
 // Quant.GatherRow (src/Needle/Quant.cs:566-576): a CQ row decoded to floats
 // (Scalar.DecodeRow, src/Needle/Scalar.cs:130-144: levels[index] * norm in
 // natural column order) and rotated back per 128-column group
@@ -396,6 +517,45 @@ int launch_cq_prepare(const float *x, int tokens, int cols, int bits, int8_t *va
     return check_launch("cq_prepare");
 }
 
+int launch_cq_matmul_jobs(const CqMatmulJob *jobs, int n_jobs, int cols, int bits, const int8_t *values,
+                          const float *scales, const float *offsets, int stride, int tokens, cudaStream_t stream) {
+    if (tokens == 0) return NDL_OK;
+    const long long token_blocks = (tokens + 7) / 8;
+    const size_t smem = (size_t)(cols / 128) * (128 + 16 + 8 + 8) * 4;  // dots, norms, scales, offsets
+    int next = 0;
+    while (next < n_jobs) {
+        CqJobList list{};
+        long long tiles = 0;
+        for (; next < n_jobs && list.n < kCqMaxJobs; next++) {
+            const CqMatmulJob &s = jobs[next];
+            if (s.row_end <= s.row_start) continue;
+            CqJob &d = list.job[list.n++];
+            d.indices = reinterpret_cast<const uint32_t *>(s.indices);
+            d.norms = s.norms;
+            d.y = s.y;
+            memcpy(d.book.bytes, s.book_bytes, 16);
+            d.book.byte_scale = s.byte_scale;
+            d.ldy = s.ldy;
+            d.row_start = s.row_start;
+            d.row_end = s.row_end;
+            d.tile_begin = (int)tiles;
+            tiles += (s.row_end - s.row_start + 15) / 16;
+        }
+        if (list.n == 0) break;
+        const long long blocks = tiles * token_blocks;
+        if (blocks > 0x7fffffffLL) return set_error(NDL_ERR_INVALID_ARG, "cq matmul: %lld CTAs", blocks);
+        if (bits == 2)
+            launch_kernel(cq_matmul_split_kernel<2>, dim3((unsigned)blocks), dim3(32 * kCqSplitWarps), smem, stream,
+                          list, cols, values, scales, offsets, stride, tokens);
+        else
+            launch_kernel(cq_matmul_split_kernel<4>, dim3((unsigned)blocks), dim3(32 * kCqSplitWarps), smem, stream,
+                          list, cols, values, scales, offsets, stride, tokens);
+        const int st = check_launch("cq_matmul_split");
+        if (st != NDL_OK) return st;
+    }
+    return NDL_OK;
+}
+
 size_t cq_matmul_smem(int cols) {
     return (size_t)kCqMaxTokens * (cols + 16) + (size_t)2 * kCqMaxTokens * (cols / 128) * 4;
 }
@@ -415,6 +575,11 @@ int launch_cq_matmul(const uint8_t *indices, const uint16_t *norms, const uint8_
     });
     if (st0 != NDL_OK) return st0;
     const int sms = device_sm_count();
+    if (tokens > kCqMaxTokens || (row_end - row_start + 15) / 16 < 8 * sms) {
+        // many tokens, or too few tiles for warp-per-tile: split the groups
+        const CqMatmulJob job{indices, norms, book_bytes, byte_scale, y, ldy, row_start, row_end};
+        return launch_cq_matmul_jobs(&job, 1, cols, bits, values, scales, offsets, stride, tokens, stream);
+    }
     CqBook book;
     memcpy(book.bytes, book_bytes, 16);
     book.byte_scale = byte_scale;

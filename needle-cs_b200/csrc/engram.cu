@@ -131,6 +131,120 @@ __global__ void __launch_bounds__(256) engram_gate_kernel(const float *__restric
     for (int i = lane; i < dim; i += 32) rt[i] = __fadd_rn(rt[i], __fmul_rn(alpha, vt[i]));
 }
 
+// CTA-per-row form of engram_gate_kernel for dim % 4 == 0, dim <= 4096 and
+// 16-byte aligned rows, the same arithmetic term for term: the rows stay in
+// registers (float4 i on thread i % 128); the squares of x and key, then the
+// products of the unit rows, go through shared memory, and thread 0 runs the
+// ascending add chains (both sums of squares interleaved, then the dot)
+// with its next float4 loads issued ahead of the current adds.
+constexpr int kGateThreads = 128;
+constexpr int kGateMaxVec = 8;
+
+__global__ void __launch_bounds__(kGateThreads) engram_gate_row_kernel(const float *__restrict__ x,
+                                                                       const float *__restrict__ key,
+                                                                       const float *__restrict__ v, int dim,
+                                                                       float *__restrict__ residual) {
+    pdl_enter();
+    __shared__ float4 sq_a[kGateThreads * kGateMaxVec], sq_b[kGateThreads * kGateMaxVec];
+    __shared__ float shared_scalar[2];
+    const int t = blockIdx.x, tid = threadIdx.x, nv = dim >> 2;
+    const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+    const float4 *xa = reinterpret_cast<const float4 *>(x + (size_t)t * dim);
+    const float4 *ka = reinterpret_cast<const float4 *>(key + (size_t)t * dim);
+    float4 xv[kGateMaxVec], kv[kGateMaxVec];
+#pragma unroll
+    for (int i = 0; i < kGateMaxVec; i++) {
+        const int idx = tid + i * kGateThreads;
+        xv[i] = idx < nv ? xa[idx] : zero;
+        kv[i] = idx < nv ? ka[idx] : zero;
+        if (idx < nv) {
+            sq_a[idx] = make_float4(__fmul_rn(xv[i].x, xv[i].x), __fmul_rn(xv[i].y, xv[i].y),
+                                    __fmul_rn(xv[i].z, xv[i].z), __fmul_rn(xv[i].w, xv[i].w));
+            sq_b[idx] = make_float4(__fmul_rn(kv[i].x, kv[i].x), __fmul_rn(kv[i].y, kv[i].y),
+                                    __fmul_rn(kv[i].z, kv[i].z), __fmul_rn(kv[i].w, kv[i].w));
+        }
+    }
+    __syncthreads();
+    if (tid == 0) {
+        float sa = 0.0f, sb = 0.0f;
+        float4 na[2], nb[2];
+#pragma unroll
+        for (int j = 0; j < 2; j++) na[j] = j < nv ? sq_a[j] : zero, nb[j] = j < nv ? sq_b[j] : zero;
+        for (int i = 0; i < nv; i += 2) {
+            float4 ca[2], cb[2];
+#pragma unroll
+            for (int j = 0; j < 2; j++) {
+                ca[j] = na[j], cb[j] = nb[j];
+                na[j] = i + 2 + j < nv ? sq_a[i + 2 + j] : zero;
+                nb[j] = i + 2 + j < nv ? sq_b[i + 2 + j] : zero;
+            }
+#pragma unroll
+            for (int j = 0; j < 2; j++)
+                if (i + j < nv) {
+                    sa = __fadd_rn(sa, ca[j].x), sb = __fadd_rn(sb, cb[j].x);
+                    sa = __fadd_rn(sa, ca[j].y), sb = __fadd_rn(sb, cb[j].y);
+                    sa = __fadd_rn(sa, ca[j].z), sb = __fadd_rn(sb, cb[j].z);
+                    sa = __fadd_rn(sa, ca[j].w), sb = __fadd_rn(sb, cb[j].w);
+                }
+        }
+        shared_scalar[0] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sa, (float)dim), 1e-6f)));
+        shared_scalar[1] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sb, (float)dim), 1e-6f)));
+    }
+    __syncthreads();
+    const float ia = shared_scalar[0], ib = shared_scalar[1];
+#pragma unroll
+    for (int i = 0; i < kGateMaxVec; i++) {
+        const int idx = tid + i * kGateThreads;
+        if (idx < nv)
+            sq_a[idx] = make_float4(__fmul_rn(__fmul_rn(xv[i].x, ia), __fmul_rn(kv[i].x, ib)),
+                                    __fmul_rn(__fmul_rn(xv[i].y, ia), __fmul_rn(kv[i].y, ib)),
+                                    __fmul_rn(__fmul_rn(xv[i].z, ia), __fmul_rn(kv[i].z, ib)),
+                                    __fmul_rn(__fmul_rn(xv[i].w, ia), __fmul_rn(kv[i].w, ib)));
+    }
+    __syncthreads();
+    if (tid == 0) {
+        float dot = 0.0f;
+        float4 nxt[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) nxt[j] = j < nv ? sq_a[j] : zero;
+        for (int i = 0; i < nv; i += 4) {
+            float4 cur[4];
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                cur[j] = nxt[j];
+                nxt[j] = i + 4 + j < nv ? sq_a[i + 4 + j] : zero;
+            }
+#pragma unroll
+            for (int j = 0; j < 4; j++)
+                if (i + j < nv) {
+                    dot = __fadd_rn(dot, cur[j].x);
+                    dot = __fadd_rn(dot, cur[j].y);
+                    dot = __fadd_rn(dot, cur[j].z);
+                    dot = __fadd_rn(dot, cur[j].w);
+                }
+        }
+        const float z = __fmul_rn(dot, __fdiv_rn(1.0f, __fsqrt_rn((float)dim)));
+        shared_scalar[0] = sigmoid_rn(z);
+    }
+    __syncthreads();
+    const float alpha = shared_scalar[0];
+    float4 *rt = reinterpret_cast<float4 *>(residual + (size_t)t * dim);
+    const float4 *vt = reinterpret_cast<const float4 *>(v + (size_t)t * dim);
+#pragma unroll
+    for (int i = 0; i < kGateMaxVec; i++) {
+        const int idx = tid + i * kGateThreads;
+        if (idx < nv) {
+            const float4 w = vt[idx];
+            float4 r = rt[idx];
+            r.x = __fadd_rn(r.x, __fmul_rn(alpha, w.x));
+            r.y = __fadd_rn(r.y, __fmul_rn(alpha, w.y));
+            r.z = __fadd_rn(r.z, __fmul_rn(alpha, w.z));
+            r.w = __fadd_rn(r.w, __fmul_rn(alpha, w.w));
+            rt[idx] = r;
+        }
+    }
+}
+
 // Quant.FakeA8 (src/Needle/Quant.cs:69-80) per row, warp per row: the row's
 // peak, then each value quantized with the reference's RoundEven (the
 // 1.5 * 2^23 bias, which also turns -0 into +0) and scaled back.
@@ -225,6 +339,12 @@ extern "C" NDL_API int ndl_engram_gate(const float *x, const float *key, const f
     NDL_REQUIRE(count >= 0 && dim >= 1, "count %d / dim %d", count, dim);
     if (count == 0) return NDL_OK;
     NDL_REQUIRE(x && key && v && residual, "null pointer");
+    if (dim % 4 == 0 && dim <= 4 * kGateThreads * kGateMaxVec && aligned(x, 16) && aligned(key, 16) &&
+        aligned(v, 16) && aligned(residual, 16)) {
+        launch_kernel(engram_gate_row_kernel, dim3((unsigned)count), dim3(kGateThreads), 0, (cudaStream_t)stream, x,
+                      key, v, dim, residual);
+        return check_launch("engram_gate_row");
+    }
     launch_kernel(engram_gate_kernel, dim3((unsigned)((count * 32LL + 255) / 256)), dim3(256), 0,
                   (cudaStream_t)stream, x, key, v, count, dim, residual);
     return check_launch("engram_gate");

@@ -102,4 +102,19 @@ int launch_gemv_i8g32(const MatmulArgs &a, cudaStream_t stream);
 // shape does not fit its tiling so the caller can fall back to the GEMV.
 int launch_gemm_i8g32_tc(const MatmulArgs &a, cudaStream_t stream);
 
+// One CQ matrix (or row slice of one) for launch_cq_matmul_jobs: rows
+// [row_start, row_end) of y [tokens][ldy] from the shared prepared
+// activations; book_bytes is the host copy of the 16 codebook bytes.
+struct CqMatmulJob {
+    const uint8_t *indices;
+    const uint16_t *norms;
+    const uint8_t *book_bytes;
+    float byte_scale;
+    float *y;
+    int ldy, row_start, row_end;
+};
+// Several matrices of the same width and bits over one Prepare, few launches.
+int launch_cq_matmul_jobs(const CqMatmulJob *jobs, int n_jobs, int cols, int bits, const int8_t *values,
+                          const float *scales, const float *offsets, int stride, int tokens, cudaStream_t stream);
+
 }  // namespace ndl

@@ -418,6 +418,22 @@ int cq_matmul(const CqView &w, const N3State *s, int tokens, int row_start, int 
     return ndl_cq_matmul(w.indices, w.norms, w.book->bytes, w.book->byte_scale, w.rows, w.cols, w.bits, s->act_values,
                          s->act_scales, s->act_offsets, s->act_stride, tokens, y, ldy, row_start, row_end, st);
 }
+// Matrices of one width over the current Prepare in as few launches as
+// their bits allow (the layer's projections share one activation Prepare).
+int cq_matmuls(const N3State *s, int tokens, const CqView *const *views, const CqMatmulJob *jobs, int n,
+               cudaStream_t st) {
+    bool same = true;
+    for (int i = 1; i < n; i++) same = same && views[i]->bits == views[0]->bits && views[i]->cols == views[0]->cols;
+    for (int i = 0; i < n; i += same ? n : 1) {
+        const int st_ = launch_cq_matmul_jobs(jobs + i, same ? n : 1, views[i]->cols, views[i]->bits, s->act_values,
+                                              s->act_scales, s->act_offsets, s->act_stride, tokens, st);
+        if (st_ != NDL_OK) return st_;
+    }
+    return NDL_OK;
+}
+CqMatmulJob cq_job(const CqView &w, int row_start, int row_end, float *y, int ldy) {
+    return CqMatmulJob{w.indices, w.norms, w.book->bytes, w.book->byte_scale, y, ldy, row_start, row_end};
+}
 int cq_prepare(N3State *s, const float *x, int tokens, int cols, int bits, cudaStream_t st) {
     return ndl_cq_prepare(x, tokens, cols, bits, s->act_values, s->act_scales, s->act_offsets, s->act_stride, st);
 }
@@ -452,9 +468,14 @@ int forward_wave(N3State *s, const int32_t *tokens, const int32_t *slots, const 
         N3_TRY(ndl_fake_a8_rows(0, s->stream, nullptr, nullptr, R, sw, s->norm4, st));
         N3_TRY(cq_prepare(s, s->norm4, R, sw, s->phi_pre.bits, st));
         // the layer's row slices of the phi matrices, into columns [4l, 4l + 4) / [16l, 16l + 16)
-        N3_TRY(cq_matmul(s->phi_pre, s, R, l * kLanes, l * kLanes + kLanes, s->pre, s->phi_pre.rows, st));
-        N3_TRY(cq_matmul(s->phi_post, s, R, l * kLanes, l * kLanes + kLanes, s->post, s->phi_post.rows, st));
-        N3_TRY(cq_matmul(s->phi_res, s, R, l * 16, l * 16 + 16, s->res, s->phi_res.rows, st));
+        {
+            const CqView *views[3] = {&s->phi_pre, &s->phi_post, &s->phi_res};
+            const CqMatmulJob jobs[3] = {
+                cq_job(s->phi_pre, l * kLanes, l * kLanes + kLanes, s->pre, s->phi_pre.rows),
+                cq_job(s->phi_post, l * kLanes, l * kLanes + kLanes, s->post, s->phi_post.rows),
+                cq_job(s->phi_res, l * 16, l * 16 + 16, s->res, s->phi_res.rows)};
+            N3_TRY(cq_matmuls(s, R, views, jobs, 3, st));
+        }
         launch_kernel(n3_gates_kernel, dim3((R + 127) / 128), dim3(128), 0, st, (const float *)s->pre,
                       s->phi_pre.rows, (const float *)s->post, s->phi_post.rows, (const float *)s->res,
                       s->phi_res.rows, s->a_pre,
@@ -476,10 +497,12 @@ int forward_wave(N3State *s, const int32_t *tokens, const int32_t *slots, const 
         // attention: prepare, projections, convs, per-head norms / RoPE / quantize, attention, gate, out, post-norm
         N3_TRY(ndl_fake_a8_rows(1, s->residual, L.norm_in, nullptr, R, d, s->norm4, st));
         N3_TRY(cq_prepare(s, s->norm4, R, d, L.q.bits, st));
-        N3_TRY(cq_matmul(L.q, s, R, 0, s->qw, s->q, s->qw, st));
-        N3_TRY(cq_matmul(L.k, s, R, 0, s->kw, s->k, s->kw, st));
-        N3_TRY(cq_matmul(L.v, s, R, 0, s->vw, s->v, s->vw, st));
-        N3_TRY(cq_matmul(L.gate, s, R, 0, s->ow, s->gate, s->ow, st));
+        {
+            const CqView *views[4] = {&L.q, &L.k, &L.v, &L.gate};
+            const CqMatmulJob jobs[4] = {cq_job(L.q, 0, s->qw, s->q, s->qw), cq_job(L.k, 0, s->kw, s->k, s->kw),
+                                         cq_job(L.v, 0, s->vw, s->v, s->vw), cq_job(L.gate, 0, s->ow, s->gate, s->ow)};
+            N3_TRY(cq_matmuls(s, R, views, jobs, 4, st));
+        }
         {
             const long long n = (long long)R * (s->qw + s->kw + s->vw);
             launch_kernel(n3_conv_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, st, s->q, s->k, s->v, slots,

@@ -62,37 +62,33 @@ __global__ void __launch_bounds__(256) combine4_kernel(const float *__restrict__
     dst[((size_t)t * kOut + o) * dim + c] = mix4_term(head, m[0], m[1], m[2], m[3], st, dim, c);
 }
 
-// Sinkhorn4x4 per token, one thread each.
+// Sinkhorn4x4 per token on 16 lanes, lane 4 * row + c holding entry (row, c):
+// each row and column sum gathers its four entries by shuffles and adds them
+// in index order, then every lane divides its own entry, so the steps and
+// roundings are the scalar loop's (Scalar.cs:361-381) with sixteen divides in
+// parallel.  Lanes past the last token run on zeros and store nothing.
 __global__ void __launch_bounds__(128) sinkhorn4x4_kernel(const float *__restrict__ logits, int n,
                                                           float *__restrict__ out) {
     pdl_enter();
-    const int t = blockIdx.x * blockDim.x + threadIdx.x;
-    if (t >= n) return;
-    const float *lg = logits + (size_t)t * 16;
-    float r[16];
-#pragma unroll
-    for (int row = 0; row < 4; row++) {
-        const float peak = fmaxf(fmaxf(lg[row * 4], lg[row * 4 + 1]), fmaxf(lg[row * 4 + 2], lg[row * 4 + 3]));
-#pragma unroll
-        for (int c = 0; c < 4; c++) r[row * 4 + c] = exp_rn(__fsub_rn(lg[row * 4 + c], peak));
-    }
+    const long long gt = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    const long long t = gt >> 4;
+    const int lane = threadIdx.x & 31, base = lane & 16, e = lane & 15, row = e >> 2, c = e & 3;
+    const bool ok = t < n;
+    const float v = ok ? logits[t * 16 + e] : 0.0f;
+    const int rl = base + 4 * row;
+    const float peak = fmaxf(fmaxf(__shfl_sync(0xffffffffu, v, rl), __shfl_sync(0xffffffffu, v, rl + 1)),
+                             fmaxf(__shfl_sync(0xffffffffu, v, rl + 2), __shfl_sync(0xffffffffu, v, rl + 3)));
+    float r = exp_rn(__fsub_rn(v, peak));
     for (int it = 0; it < 20; it++) {
-#pragma unroll
-        for (int row = 0; row < 4; row++) {
-            const float sum = __fadd_rn(__fadd_rn(__fadd_rn(r[row * 4], r[row * 4 + 1]), r[row * 4 + 2]), r[row * 4 + 3]);
-#pragma unroll
-            for (int c = 0; c < 4; c++) r[row * 4 + c] = __fdiv_rn(r[row * 4 + c], sum);
-        }
-#pragma unroll
-        for (int c = 0; c < 4; c++) {
-            const float sum = __fadd_rn(__fadd_rn(__fadd_rn(r[c], r[4 + c]), r[8 + c]), r[12 + c]);
-            if (sum > 0.0f)
-#pragma unroll
-                for (int row = 0; row < 4; row++) r[row * 4 + c] = __fdiv_rn(r[row * 4 + c], sum);
-        }
+        const float a0 = __shfl_sync(0xffffffffu, r, rl), a1 = __shfl_sync(0xffffffffu, r, rl + 1);
+        const float a2 = __shfl_sync(0xffffffffu, r, rl + 2), a3 = __shfl_sync(0xffffffffu, r, rl + 3);
+        r = __fdiv_rn(r, __fadd_rn(__fadd_rn(__fadd_rn(a0, a1), a2), a3));
+        const float b0 = __shfl_sync(0xffffffffu, r, base + c), b1 = __shfl_sync(0xffffffffu, r, base + 4 + c);
+        const float b2 = __shfl_sync(0xffffffffu, r, base + 8 + c), b3 = __shfl_sync(0xffffffffu, r, base + 12 + c);
+        const float sum = __fadd_rn(__fadd_rn(__fadd_rn(b0, b1), b2), b3);
+        if (sum > 0.0f) r = __fdiv_rn(r, sum);
     }
-#pragma unroll
-    for (int k = 0; k < 16; k++) out[(size_t)t * 16 + k] = r[k];
+    if (ok) out[t * 16 + e] = r;
 }
 
 // Taps3 on triples [n][3][width] = (x_{t-2}, x_{t-1}, x_t).
@@ -154,6 +150,138 @@ __global__ void __launch_bounds__(256) fake_a8_kernel(const float *__restrict__ 
         // turns -0 into +0 (rintf would keep the sign of a zero)
         const float r = __fsub_rn(__fadd_rn(__fmul_rn(dr[i], round), 12582912.0f), 12582912.0f);
         dr[i] = __fmul_rn(fminf(fmaxf(r, -128.0f), 127.0f), scale);
+    }
+}
+
+// CTA-per-row form of fake_a8_kernel for rows of n % 4 == 0, n <= 4096 floats
+// on 16-byte boundaries, with the same arithmetic element for element: the
+// row stays in registers (float4 i on thread i % 128), the squares go through
+// shared memory and thread 0 sums them in ascending order with its next four
+// float4 loads issued ahead of the current adds (the add chain is the
+// kernel's critical path); the peak is a max over the CTA.
+constexpr int kFakeThreads = 128;
+constexpr int kFakeMaxVec = 8;
+
+__device__ __forceinline__ float fake_warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(kFakeThreads) fake_a8_row_kernel(const float *__restrict__ x,
+                                                                   const float *__restrict__ aux,
+                                                                   const float *__restrict__ gate, int n,
+                                                                   float *__restrict__ dst) {
+    pdl_enter();
+    __shared__ float red[kFakeThreads / 32];
+    __shared__ float4 squares[MODE == 2 ? 1 : kFakeThreads * kFakeMaxVec];
+    const int row = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nv = n >> 2;
+    const float4 *in = reinterpret_cast<const float4 *>(x + (size_t)row * n);
+    const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+    float4 v[kFakeMaxVec];
+#pragma unroll
+    for (int i = 0; i < kFakeMaxVec; i++) {
+        const int idx = tid + i * kFakeThreads;
+        v[i] = idx < nv ? in[idx] : zero;
+    }
+    float inverse = 0.0f;
+    if (MODE != 2) {
+#pragma unroll
+        for (int i = 0; i < kFakeMaxVec; i++) {
+            const int idx = tid + i * kFakeThreads;
+            if (idx < nv)
+                squares[idx] = make_float4(__fmul_rn(v[i].x, v[i].x), __fmul_rn(v[i].y, v[i].y),
+                                           __fmul_rn(v[i].z, v[i].z), __fmul_rn(v[i].w, v[i].w));
+        }
+        __syncthreads();
+        if (tid == 0) {
+            float sum = 0.0f;
+            float4 nxt[4];
+#pragma unroll
+            for (int j = 0; j < 4; j++) nxt[j] = j < nv ? squares[j] : zero;
+            for (int i = 0; i < nv; i += 4) {
+                float4 cur[4];
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    cur[j] = nxt[j];
+                    nxt[j] = i + 4 + j < nv ? squares[i + 4 + j] : zero;
+                }
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    if (i + j < nv) {
+                        sum = __fadd_rn(sum, cur[j].x);
+                        sum = __fadd_rn(sum, cur[j].y);
+                        sum = __fadd_rn(sum, cur[j].z);
+                        sum = __fadd_rn(sum, cur[j].w);
+                    }
+                }
+            }
+            red[0] = sum;
+        }
+        __syncthreads();
+        const float sum = red[0];
+        __syncthreads();  // red is reused for the peak
+        inverse = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, (float)n), 1e-6f)));
+    }
+    if (MODE == 3) {
+        const float g = gate[row];
+        const float4 *sv = reinterpret_cast<const float4 *>(aux);
+        float4 *dv = reinterpret_cast<float4 *>(dst + (size_t)row * n);
+#pragma unroll
+        for (int i = 0; i < kFakeMaxVec; i++) {
+            const int idx = tid + i * kFakeThreads;
+            if (idx < nv) {
+                const float4 s = sv[idx];
+                float4 o = dv[idx];
+                o.x = __fadd_rn(o.x, __fmul_rn(g, __fmul_rn(__fmul_rn(__fadd_rn(1.0f, s.x), v[i].x), inverse)));
+                o.y = __fadd_rn(o.y, __fmul_rn(g, __fmul_rn(__fmul_rn(__fadd_rn(1.0f, s.y), v[i].y), inverse)));
+                o.z = __fadd_rn(o.z, __fmul_rn(g, __fmul_rn(__fmul_rn(__fadd_rn(1.0f, s.z), v[i].z), inverse)));
+                o.w = __fadd_rn(o.w, __fmul_rn(g, __fmul_rn(__fmul_rn(__fadd_rn(1.0f, s.w), v[i].w), inverse)));
+                dv[idx] = o;
+            }
+        }
+        return;
+    }
+    float peak = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kFakeMaxVec; i++) {
+        const int idx = tid + i * kFakeThreads;
+        if (idx < nv) {
+            float *e = reinterpret_cast<float *>(&v[i]);
+            float4 a = zero;
+            if (MODE == 1) a = reinterpret_cast<const float4 *>(aux)[idx];
+            if (MODE == 2) a = reinterpret_cast<const float4 *>(aux + (size_t)row * n)[idx];
+            const float *av = reinterpret_cast<const float *>(&a);
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                if (MODE == 0) e[k] = __fmul_rn(e[k], inverse);
+                else if (MODE == 1) e[k] = __fmul_rn(__fmul_rn(__fadd_rn(1.0f, av[k]), e[k]), inverse);
+                else e[k] = __fmul_rn(e[k], sigmoid_rn(av[k]));
+                peak = fmaxf(peak, fabsf(e[k]));
+            }
+        }
+    }
+    peak = fake_warp_max(peak);
+    if (lane == 0) red[warp] = peak;
+    __syncthreads();
+    peak = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+    const float scale = peak > 0.0f ? __fdiv_rn(peak, 127.0f) : 1.0f;
+    const float round = __fdiv_rn(1.0f, scale);
+    float4 *dv = reinterpret_cast<float4 *>(dst + (size_t)row * n);
+#pragma unroll
+    for (int i = 0; i < kFakeMaxVec; i++) {
+        const int idx = tid + i * kFakeThreads;
+        if (idx < nv) {
+            float *e = reinterpret_cast<float *>(&v[i]);
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                // Scalar.RoundEven as in fake_a8_kernel
+                const float r = __fsub_rn(__fadd_rn(__fmul_rn(e[k], round), 12582912.0f), 12582912.0f);
+                e[k] = __fmul_rn(fminf(fmaxf(r, -128.0f), 127.0f), scale);
+            }
+            dv[idx] = v[i];
+        }
     }
 }
 
@@ -377,22 +505,54 @@ struct KtMlpArgs {
     long long row_stride;  // block b updates residual + b * row_stride (0: one row)
 };
 
+// One Kronecker factor pair: tmp = left^T z (active_rows of z), then
+// result = tmp right, every element a sum in ascending index order.  Each
+// thread runs the chains of up to four elements (blockDim apart) side by
+// side so their loads and adds overlap.
 __device__ void mlp_kron(const float *z, int active_rows, const float *left, const float *right, int rows, int cols,
                          int result_rows, float *tmp, float *result) {
-    for (int e = threadIdx.x; e < result_rows * cols; e += blockDim.x) {
-        const int k = e / cols, c = e - k * cols;
-        float sum = 0.0f;
-        for (int i = 0; i < active_rows; i++) sum = __fadd_rn(sum, __fmul_rn(left[i * rows + k], z[i * cols + c]));
-        tmp[e] = sum;
+    const int n = result_rows * cols;
+    for (int e0 = threadIdx.x; e0 < n; e0 += 4 * blockDim.x) {
+        int kq[4], cq[4];
+        float sum[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            const int e = min(e0 + q * (int)blockDim.x, n - 1);
+            kq[q] = e / cols;
+            cq[q] = e - kq[q] * cols;
+        }
+        for (int i = 0; i < active_rows; i++)
+#pragma unroll
+            for (int q = 0; q < 4; q++) sum[q] = __fadd_rn(sum[q], __fmul_rn(left[i * rows + kq[q]], z[i * cols + cq[q]]));
+#pragma unroll
+        for (int q = 0; q < 4; q++)
+            if (e0 + q * (int)blockDim.x < n) tmp[e0 + q * blockDim.x] = sum[q];
     }
     __syncthreads();
-    for (int e = threadIdx.x; e < result_rows * cols; e += blockDim.x) {
-        const int k = e / cols, c = e - k * cols;
-        float sum = 0.0f;
-        for (int j = 0; j < cols; j++) sum = __fadd_rn(sum, __fmul_rn(tmp[k * cols + j], right[j * cols + c]));
-        result[e] = sum;
+    for (int e0 = threadIdx.x; e0 < n; e0 += 4 * blockDim.x) {
+        int kq[4], cq[4];
+        float sum[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            const int e = min(e0 + q * (int)blockDim.x, n - 1);
+            kq[q] = e / cols;
+            cq[q] = e - kq[q] * cols;
+        }
+        for (int j = 0; j < cols; j++)
+#pragma unroll
+            for (int q = 0; q < 4; q++) sum[q] = __fadd_rn(sum[q], __fmul_rn(tmp[kq[q] * cols + j], right[j * cols + cq[q]]));
+#pragma unroll
+        for (int q = 0; q < 4; q++)
+            if (e0 + q * (int)blockDim.x < n) result[e0 + q * blockDim.x] = sum[q];
     }
     __syncthreads();
+}
+
+// Shared floats of slot_hadamard_mlp_kernel: weights[8], normalized[dim],
+// front / back / tmp [width] and scratch[8 * dim] (squares, then the
+// ConditionWeights products).
+__host__ __device__ inline size_t mlp_smem_floats(int dim, int width) {
+    return 8 + (size_t)dim + 3 * (size_t)width + 8 * (size_t)dim;
 }
 
 __global__ void __launch_bounds__(256) slot_hadamard_mlp_kernel(KtMlpArgs a) {
@@ -402,21 +562,32 @@ __global__ void __launch_bounds__(256) slot_hadamard_mlp_kernel(KtMlpArgs a) {
     const int input_rows = (dim + cols - 1) / cols;
     const int output_rows = min(rows, (input_rows + 3) / 4 * 4);
     float *weights = sm, *normalized = sm + 8, *front = normalized + dim, *back = front + width, *tmp = back + width;
+    float *scratch = tmp + width;
     const float *d1 = a.w[0], *d2 = a.w[1], *b2 = a.w[2], *d3 = a.w[3], *d4 = a.w[4];
-    if (threadIdx.x == 0) {  // ZeroCenteredRms: the sum of squares in order
+    // ZeroCenteredRms: the squares in parallel, their sum in order on thread 0
+    for (int i = threadIdx.x; i < dim; i += blockDim.x) {
+        const float r = residual[i];
+        scratch[i] = __fmul_rn(r, r);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
         float sum = 0.0f;
-        for (int i = 0; i < dim; i++) sum = __fadd_rn(sum, __fmul_rn(residual[i], residual[i]));
+#pragma unroll 16
+        for (int i = 0; i < dim; i++) sum = __fadd_rn(sum, scratch[i]);
         weights[0] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, (float)dim), 1e-6f)));
     }
     __syncthreads();
     const float inv = weights[0];
-    __syncthreads();
     for (int i = threadIdx.x; i < dim; i += blockDim.x)
         normalized[i] = __fmul_rn(__fmul_rn(__fadd_rn(1.0f, a.pre_norm[i]), residual[i]), inv);
     __syncthreads();
-    if (threadIdx.x < 8) {  // ConditionWeights
+    // ConditionWeights: products in parallel, weight j summed in order by thread j
+    for (int e = threadIdx.x; e < dim * 8; e += blockDim.x) scratch[e] = __fmul_rn(normalized[e >> 3], a.w[11][e]);
+    __syncthreads();
+    if (threadIdx.x < 8) {
         float sum = 0.0f;
-        for (int i = 0; i < dim; i++) sum = __fadd_rn(sum, __fmul_rn(normalized[i], a.w[11][i * 8 + threadIdx.x]));
+#pragma unroll 16
+        for (int i = 0; i < dim; i++) sum = __fadd_rn(sum, scratch[i * 8 + threadIdx.x]);
         weights[threadIdx.x] = sum;
     }
     __syncthreads();
@@ -449,7 +620,7 @@ __global__ void __launch_bounds__(256) slot_hadamard_mlp_kernel(KtMlpArgs a) {
 }
 
 int launch_slot_hadamard_mlp(const KtMlpArgs &a, cudaStream_t stream) {
-    const size_t smem = (size_t)(8 + a.dim + 3 * a.rows * a.cols) * 4;
+    const size_t smem = mlp_smem_floats(a.dim, a.rows * a.cols) * 4;
     if (smem > 200 * 1024) return set_error(NDL_ERR_UNSUPPORTED, "hadamard_mlp: dim %d x width %d too large", a.dim,
                                             a.rows * a.cols);
     cudaFuncSetAttribute(slot_hadamard_mlp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -479,7 +650,7 @@ int launch_combine4(bool diff, const float *s, int dim, const float *mix, const 
 }
 int launch_sinkhorn4x4(const float *logits, int n, float *out, cudaStream_t stream) {
     if (n == 0) return NDL_OK;
-    launch_kernel(sinkhorn4x4_kernel, dim3(blocks_for(n, 128)), dim3(128), 0, stream, logits, n, out);
+    launch_kernel(sinkhorn4x4_kernel, dim3(blocks_for((long long)n * 16, 128)), dim3(128), 0, stream, logits, n, out);
     return check_launch("sinkhorn4x4");
 }
 int launch_taps3(const float *taps, int width, const float *triples, int n, float *dst, cudaStream_t stream) {
@@ -491,6 +662,17 @@ int launch_taps3(const float *taps, int width, const float *triples, int n, floa
 int launch_fake_a8(int mode, const float *x, const float *aux, const float *gate, int rows, int n, float *dst,
                    cudaStream_t stream) {
     if (rows == 0) return NDL_OK;
+    if (n % 4 == 0 && n <= 4 * kFakeThreads * kFakeMaxVec && aligned(x, 16) && aligned(dst, 16) &&
+        (mode == 0 || aligned(aux, 16))) {
+        const dim3 grid((unsigned)rows), block(kFakeThreads);
+        switch (mode) {
+            case 0: launch_kernel(fake_a8_row_kernel<0>, grid, block, 0, stream, x, aux, gate, n, dst); break;
+            case 1: launch_kernel(fake_a8_row_kernel<1>, grid, block, 0, stream, x, aux, gate, n, dst); break;
+            case 2: launch_kernel(fake_a8_row_kernel<2>, grid, block, 0, stream, x, aux, gate, n, dst); break;
+            default: launch_kernel(fake_a8_row_kernel<3>, grid, block, 0, stream, x, aux, gate, n, dst); break;
+        }
+        return check_launch("fake_a8_row");
+    }
     const dim3 grid(blocks_for((long long)rows * 32, 256)), block(256);
     switch (mode) {
         case 0: launch_kernel(fake_a8_kernel<0>, grid, block, 0, stream, x, aux, gate, rows, n, dst); break;
@@ -598,7 +780,7 @@ extern "C" NDL_API int ndl_mlp_apply(const ndl_model *m, int layer, float *resid
     a.scale = scale;
     a.residual = residual;
     a.row_stride = dim;
-    const size_t smem = (size_t)(8 + dim + 3 * width) * 4;
+    const size_t smem = mlp_smem_floats(dim, width) * 4;
     if (smem > 200 * 1024) return set_error(NDL_ERR_UNSUPPORTED, "hadamard_mlp: dim %d x width %d too large", dim, width);
     NDL_CUDA(cudaFuncSetAttribute(slot_hadamard_mlp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     slot_hadamard_mlp_kernel<<<(unsigned)count, 256, smem, (cudaStream_t)stream>>>(a);

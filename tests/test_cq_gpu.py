@@ -95,6 +95,10 @@ def test_prepare_matches_oracle(lib, oracle, bits, tokens, cols):
 MATMUL_CASES = [  # (bits, rows, cols, tokens): the conformance shapes, then decode-sized ones
     (2, 5, 768, 1), (2, 5, 768, 3), (4, 7, 384, 5), (2, 3, 128, 8), (4, 97, 768, 3), (2, 5, 768, 0),
     (2, 2048, 512, 1), (4, 2048, 512, 16), (2, 512, 4096, 2), (4, 1000, 1024, 20),
+    # many tokens (8-token blocks, a ragged last block) and long rows: the group-split kernel
+    (2, 600, 768, 64), (4, 40, 3072, 33), (2, 24, 8192, 9),
+    # enough 16-row tiles for the warp-per-tile kernel (<= 16 tokens)
+    (2, 20000, 256, 5), (4, 19000, 128, 16),
 ]
 
 

@@ -88,13 +88,14 @@ def test_engram_conv_matches_oracle(dev, oracle, dilation):
     assert np.array_equal(hout.cpu().numpy().view(np.uint32), want_hist.view(np.uint32))
 
 
-def test_engram_gate_matches_oracle(dev, oracle):
+@pytest.mark.parametrize("dim", [768, 130])  # the CTA-per-row kernel; a width it does not take
+def test_engram_gate_matches_oracle(dev, oracle, dim):
     import torch
 
     from needle_cs_b200 import _native
 
     rng = np.random.default_rng(5)
-    count, dim = 37, 768
+    count = 37
     x = rng.normal(size=(count, dim)).astype(np.float32)
     key = (x * 0.5 + rng.normal(size=(count, dim))).astype(np.float32)
     v = rng.normal(size=(count, dim)).astype(np.float32)

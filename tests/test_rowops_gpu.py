@@ -164,6 +164,30 @@ def test_batched_device_entry_points(pkg, olib, oracle):
         assert np.array_equal(_bits(rh[r]), _bits(ref)), r
 
 
+@pytest.mark.parametrize("width", [384, 3072, 4100, 770])  # CTA-per-row kernel, then widths it does not take
+def test_fake_a8_rows_batched(pkg, oracle, width):
+    """ndl_fake_a8_rows modes 0 and 2 over many rows (mode 2: one gate row per
+    row) equal the oracle's rows bit for bit."""
+    import torch
+
+    from needle_cs_b200 import _native
+
+    dev = torch.device("cuda:0")
+    rows = 19
+    rng = np.random.default_rng(width)
+    xh = (rng.normal(size=(rows, width)) * 3).astype(np.float32)
+    gh = (rng.normal(size=(rows, width)) * 4).astype(np.float32)
+    xr, gr = torch.from_numpy(xh).to(dev), torch.from_numpy(gh).to(dev)
+    out = [torch.empty((rows, width), device=dev) for _ in range(2)]
+    _native.call("ndl_fake_a8_rows", 0, xr.data_ptr(), None, None, rows, width, out[0].data_ptr(), None)
+    _native.call("ndl_fake_a8_rows", 2, xr.data_ptr(), gr.data_ptr(), None, rows, width, out[1].data_ptr(), None)
+    torch.cuda.synchronize()
+    f0, f2 = out[0].cpu().numpy(), out[1].cpu().numpy()
+    for r in range(rows):
+        assert np.array_equal(_bits(f0[r]), _bits(oracle.fake_a8_row(0, xh[r]))), r
+        assert np.array_equal(_bits(f2[r]), _bits(oracle.fake_a8_row(2, xh[r], gh[r]))), r
+
+
 def test_float_helper_slots(lib, olib, oracle, golden):
     """Slots 14-21 and 23 against the oracle and the reference's goldens."""
     fx = golden["fixtures"]
