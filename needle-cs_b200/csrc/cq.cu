@@ -15,21 +15,16 @@
 //   scaled = (norm[g] * byte_scale) * scale[t][g]
 //   acc += scaled * dot;  bias += scaled * offset[t][g];   y = acc - bias.
 #include "common.cuh"
+#include "cq.cuh"
 #include "kernels.cuh"
 
 namespace ndl {
 
-constexpr float kCqHadamardScale = 0.08838834764831845f;  // Scalar.cs:49 (Quant.cs:51)
 constexpr int kCqMaxTokens = 16;                          // tokens per matmul launch (lane t folds token t)
 constexpr int kCqWarps = 8;
 constexpr int kCqMaxCols = 8192;
-constexpr int kCqSplitWarps = 4;  // warps per CTA of cq_matmul_split_kernel (they split the groups)
+constexpr int kCqSplitMaxWarps = 8;  // warps per CTA of cq_matmul_split_kernel at most
 constexpr int kCqMaxJobs = 4;     // matrices per cq_matmul_split_kernel launch
-
-__device__ __forceinline__ int8_t cq_quant1(float x, float inverse) {
-    const float r = rintf(__fmul_rn(x, inverse));
-    return (int8_t)(int)fminf(fmaxf(r, -128.0f), 127.0f);
-}
 
 // Scalar.Hadamard's butterflies (src/Needle/Scalar.cs:76-89) on a warp's
 // 128 values, lane l holding elements l, l+32, l+64, l+96: strides 1, 2, ...,
@@ -92,9 +87,7 @@ __global__ void __launch_bounds__(256) cq_prepare_kernel(const float *__restrict
     for (int k = 0; k < 4; k++) {
         const int8_t q = cq_quant1(v[k], inverse);
         const int e = lane + 32 * k;
-        // Planes: 2-bit [p*32 + j] = q[4j + p]; 4-bit [h*64 + p*32 + j] = q[h*64 + 2j + p]
-        const int at = bits == 2 ? (e & 3) * 32 + (e >> 2) : (e >> 6) * 64 + (e & 1) * 32 + ((e & 63) >> 1);
-        dst[at] = q;
+        dst[cq_plane_at(e, bits)] = q;
         sum += q;
     }
 #pragma unroll
@@ -353,51 +346,57 @@ struct CqJobList {
     int n;
 };
 
-// The same MatMulRows for many tokens or few rows: CTA per (job, 16-row
-// tile, 8-token block).  Its warps split the 128-column groups (warp w takes
-// groups w, w + kCqSplitWarps, ...): per group the A fragments as in
+// The same MatMulRows for many tokens or few rows.  A CTA takes one 16-row
+// tile of one job and `tbs` 8-token blocks; its warps are (token block,
+// group phase) pairs, `split` phases per block, so warp (b, p) takes groups
+// p, p + split, ... of block b.  Per group: the A fragments as in
 // cq_matmul_kernel, the B fragments loaded straight from the prepared values
 // (each lane's eight words g*128 + 4*tig + 16*j of its token; for 2-bit the
 // plane permutation of cq_matmul_kernel's staging done with byte permutes),
 // four mma.sync, and the exact int32 dots left in shared memory with the
-// rows' norm * byte_scale and the tokens' scales and offsets.  Then thread
-// (row, token) folds the groups in ascending order with the same fp32 steps
-// as cq_matmul_kernel (Scalar.MatMulRows, src/Needle/Scalar.cs:146-192).
+// rows' norm * byte_scale and the tokens' scales and offsets.  Then each
+// (row, token) is folded over the groups in ascending order with the same
+// fp32 steps as cq_matmul_kernel (Scalar.MatMulRows,
+// src/Needle/Scalar.cs:146-192).
 template <int kBits>
-__global__ void __launch_bounds__(32 * kCqSplitWarps) cq_matmul_split_kernel(
+__global__ void __launch_bounds__(32 * kCqSplitMaxWarps) cq_matmul_split_kernel(
     CqJobList jobs, int cols, const int8_t *__restrict__ values, const float *__restrict__ scales,
-    const float *__restrict__ offsets, int stride, int tokens) {
+    const float *__restrict__ offsets, int stride, int tokens, int split) {
     extern __shared__ __align__(16) uint8_t smem[];
     const int groups = cols / 128, row_words = cols * kBits / 32;
     constexpr int kGroupWords = kBits == 2 ? 8 : 16;
     constexpr int kBlocks = kBits == 2 ? 1 : 2;
-    const int token_blocks = (tokens + 7) >> 3;
-    const int tile = blockIdx.x / token_blocks, tb = blockIdx.x - tile * token_blocks;
+    const int tbs = (int)(blockDim.x >> 5) / split, token_blocks = (tokens + 7) >> 3;
+    const int ctas_per_tile = (token_blocks + tbs - 1) / tbs;
+    const int tile = blockIdx.x / ctas_per_tile, tb0 = (blockIdx.x - tile * ctas_per_tile) * tbs;
     CqJob job = jobs.job[0];
 #pragma unroll
     for (int i = 1; i < kCqMaxJobs; i++)
         if (i < jobs.n && tile >= jobs.job[i].tile_begin) job = jobs.job[i];
     const int r_base = job.row_start + (tile - job.tile_begin) * 16;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
-    int *dots = reinterpret_cast<int *>(smem);                   // [groups][16 rows][8 tokens]
-    float *nf = reinterpret_cast<float *>(dots + groups * 128);  // [groups][16]
-    float *ss = nf + groups * 16;                                // [groups][8]
-    float *os = ss + groups * 8;                                 // [groups][8]
-    const int r0 = r_base + gid, r1 = r0 + 8, t = tb * 8 + gid;
+    const int tl = warp / split, phase = warp - tl * split;
+    int *dots = reinterpret_cast<int *>(smem);                         // [tbs][groups][16 rows][8 tokens]
+    float *nf = reinterpret_cast<float *>(dots + tbs * groups * 128);  // [groups][16]
+    float *ss = nf + groups * 16;                                      // [tbs][groups][8]
+    float *os = ss + tbs * groups * 8;                                 // [tbs][groups][8]
+    const int r0 = r_base + gid, r1 = r0 + 8, t = (tb0 + tl) * 8 + gid;
     const bool ok0 = r0 < job.row_end, ok1 = r1 < job.row_end, okt = t < tokens;
     const uint32_t *w0 = job.indices + (size_t)(ok0 ? r0 : job.row_start) * row_words;
     const uint32_t *w1 = job.indices + (size_t)(ok1 ? r1 : job.row_start) * row_words;
     const uint32_t *xw = reinterpret_cast<const uint32_t *>(values + (size_t)(okt ? t : 0) * cols) + tig;
-    // one side value per lane and group: lanes 0..15 a row's norm * byte_scale,
-    // 16..23 a token's scale, 24..31 its offset
-    const int side_row = r_base + (lane & 15), side_tok = tb * 8 + (lane & 7);
+    // one side value per lane and group: lanes 0..15 a row's norm * byte_scale
+    // (written by the first block's warps), 16..23 a token's scale, 24..31 its offset
+    const int side_row = r_base + (lane & 15), side_tok = (tb0 + tl) * 8 + (lane & 7);
     const bool side_ok = lane < 16 ? side_row < job.row_end : side_tok < tokens;
+    const bool side_writes = lane >= 16 || tl == 0;
     const float *side_src = lane < 24 ? scales : offsets;
-    float *side_dst = lane < 16 ? nf + lane : lane < 24 ? ss + (lane - 16) : os + (lane - 24);
+    float *side_dst = lane < 16 ? nf + lane : (lane < 24 ? ss : os) + (size_t)tl * groups * 8 + (lane & 7);
     const int side_step = lane < 16 ? 16 : 8;
+    int *my_dots = dots + (size_t)tl * groups * 128;
     pdl_enter();
 #pragma unroll 2
-    for (int g = warp; g < groups; g += kCqSplitWarps) {
+    for (int g = phase; g < groups; g += split) {
         uint32_t c0[kBlocks][2], c1[kBlocks][2], x[8];
 #pragma unroll
         for (int h = 0; h < kBlocks; h++) {
@@ -410,7 +409,7 @@ __global__ void __launch_bounds__(32 * kCqSplitWarps) cq_matmul_split_kernel(
 #pragma unroll
         for (int j = 0; j < 8; j++) x[j] = okt ? __ldg(xw + g * 32 + 4 * j) : 0u;
         float side = 0.0f;
-        if (side_ok)
+        if (side_ok && side_writes)
             side = lane < 16 ? __fmul_rn(half_to_float_ref_fast(job.norms[(size_t)side_row * groups + g]),
                                          job.book.byte_scale)
                              : side_src[(size_t)side_tok * stride + g];
@@ -441,21 +440,24 @@ __global__ void __launch_bounds__(32 * kCqSplitWarps) cq_matmul_split_kernel(
             }
         }
         // rows gid, gid + 8; tokens 2 tig, 2 tig + 1
-        *reinterpret_cast<int2 *>(dots + g * 128 + gid * 8 + 2 * tig) = make_int2(d[0], d[1]);
-        *reinterpret_cast<int2 *>(dots + g * 128 + (gid + 8) * 8 + 2 * tig) = make_int2(d[2], d[3]);
-        side_dst[g * side_step] = side;
+        *reinterpret_cast<int2 *>(my_dots + g * 128 + gid * 8 + 2 * tig) = make_int2(d[0], d[1]);
+        *reinterpret_cast<int2 *>(my_dots + g * 128 + (gid + 8) * 8 + 2 * tig) = make_int2(d[2], d[3]);
+        if (side_writes) side_dst[g * side_step] = side;
     }
     __syncthreads();
-    if (threadIdx.x >= 128) return;
-    const int r = threadIdx.x >> 3, tk = threadIdx.x & 7;
-    float acc = 0.0f, bias = 0.0f;
-    for (int g = 0; g < groups; g++) {
-        const float scaled = __fmul_rn(nf[g * 16 + r], ss[g * 8 + tk]);
-        acc = __fadd_rn(acc, __fmul_rn(scaled, (float)dots[g * 128 + r * 8 + tk]));
-        bias = __fadd_rn(bias, __fmul_rn(scaled, os[g * 8 + tk]));
+    for (int q = threadIdx.x; q < tbs * 128; q += blockDim.x) {
+        const int b = q >> 7, r = (q >> 3) & 15, tk = q & 7;
+        const int *bd = dots + (size_t)b * groups * 128 + r * 8 + tk;
+        const float *bs = ss + (size_t)b * groups * 8 + tk, *bo = os + (size_t)b * groups * 8 + tk;
+        float acc = 0.0f, bias = 0.0f;
+        for (int g = 0; g < groups; g++) {
+            const float scaled = __fmul_rn(nf[g * 16 + r], bs[g * 8]);
+            acc = __fadd_rn(acc, __fmul_rn(scaled, (float)bd[g * 128]));
+            bias = __fadd_rn(bias, __fmul_rn(scaled, bo[g * 8]));
+        }
+        const int row = r_base + r, tok = (tb0 + b) * 8 + tk;
+        if (row < job.row_end && tok < tokens) job.y[(size_t)tok * job.ldy + row] = __fsub_rn(acc, bias);
     }
-    const int row = r_base + r, tok = tb * 8 + tk;
-    if (row < job.row_end && tok < tokens) job.y[(size_t)tok * job.ldy + row] = __fsub_rn(acc, bias);
 }
 
 // Quant.GatherRow (src/Needle/Quant.cs:566-576): a CQ row decoded to floats
@@ -520,8 +522,13 @@ int launch_cq_prepare(const float *x, int tokens, int cols, int bits, int8_t *va
 int launch_cq_matmul_jobs(const CqMatmulJob *jobs, int n_jobs, int cols, int bits, const int8_t *values,
                           const float *scales, const float *offsets, int stride, int tokens, cudaStream_t stream) {
     if (tokens == 0) return NDL_OK;
-    const long long token_blocks = (tokens + 7) / 8;
-    const size_t smem = (size_t)(cols / 128) * (128 + 16 + 8 + 8) * 4;  // dots, norms, scales, offsets
+    const int groups = cols / 128, token_blocks = (tokens + 7) / 8;
+    // group phases per token block: about three groups per warp; token blocks
+    // per CTA fill it up to kCqSplitMaxWarps warps
+    const int split = groups >= 24 ? 8 : groups >= 12 ? 4 : groups >= 6 ? 2 : 1;
+    const int tbs = kCqSplitMaxWarps / split < token_blocks ? kCqSplitMaxWarps / split : token_blocks;
+    const long long ctas_per_tile = (token_blocks + tbs - 1) / tbs;
+    const size_t smem = ((size_t)tbs * groups * (128 + 16) + (size_t)groups * 16) * 4;  // dots, scales, offsets, norms
     int next = 0;
     while (next < n_jobs) {
         CqJobList list{};
@@ -542,14 +549,14 @@ int launch_cq_matmul_jobs(const CqMatmulJob *jobs, int n_jobs, int cols, int bit
             tiles += (s.row_end - s.row_start + 15) / 16;
         }
         if (list.n == 0) break;
-        const long long blocks = tiles * token_blocks;
+        const long long blocks = tiles * ctas_per_tile;
         if (blocks > 0x7fffffffLL) return set_error(NDL_ERR_INVALID_ARG, "cq matmul: %lld CTAs", blocks);
         if (bits == 2)
-            launch_kernel(cq_matmul_split_kernel<2>, dim3((unsigned)blocks), dim3(32 * kCqSplitWarps), smem, stream,
-                          list, cols, values, scales, offsets, stride, tokens);
+            launch_kernel(cq_matmul_split_kernel<2>, dim3((unsigned)blocks), dim3(32 * split * tbs), smem, stream,
+                          list, cols, values, scales, offsets, stride, tokens, split);
         else
-            launch_kernel(cq_matmul_split_kernel<4>, dim3((unsigned)blocks), dim3(32 * kCqSplitWarps), smem, stream,
-                          list, cols, values, scales, offsets, stride, tokens);
+            launch_kernel(cq_matmul_split_kernel<4>, dim3((unsigned)blocks), dim3(32 * split * tbs), smem, stream,
+                          list, cols, values, scales, offsets, stride, tokens, split);
         const int st = check_launch("cq_matmul_split");
         if (st != NDL_OK) return st;
     }

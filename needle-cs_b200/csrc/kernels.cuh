@@ -113,6 +113,11 @@ struct CqMatmulJob {
     float *y;
     int ldy, row_start, row_end;
 };
+// ndl_fake_a8_rows modes 0..2 followed by CQ Prepare of the rows, in one
+// launch; NDL_ERR_UNSUPPORTED (nothing launched) unless n % 128 == 0,
+// n <= 4096 and x / aux sit on 16-byte boundaries.
+int launch_fake_a8_prepare(int mode, const float *x, const float *aux, int rows, int n, int bits, int8_t *values,
+                           float *scales, float *offsets, int stride, cudaStream_t stream);
 // Several matrices of the same width and bits over one Prepare, few launches.
 int launch_cq_matmul_jobs(const CqMatmulJob *jobs, int n_jobs, int cols, int bits, const int8_t *values,
                           const float *scales, const float *offsets, int stride, int tokens, cudaStream_t stream);

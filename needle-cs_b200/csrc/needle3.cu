@@ -418,6 +418,17 @@ int cq_matmul(const CqView &w, const N3State *s, int tokens, int row_start, int 
     return ndl_cq_matmul(w.indices, w.norms, w.book->bytes, w.book->byte_scale, w.rows, w.cols, w.bits, s->act_values,
                          s->act_scales, s->act_offsets, s->act_stride, tokens, y, ldy, row_start, row_end, st);
 }
+int cq_prepare(N3State *s, const float *x, int tokens, int cols, int bits, cudaStream_t st);
+// A fake-A8 row op (modes 0..2) and the CQ Prepare of its output: one
+// launch where the width allows, else the two steps through `tmp`.
+int fake_a8_prepare(N3State *s, int mode, const float *x, const float *aux, int rows, int n, int bits, float *tmp,
+                    cudaStream_t st) {
+    const int rc = launch_fake_a8_prepare(mode, x, aux, rows, n, bits, s->act_values, s->act_scales, s->act_offsets,
+                                          s->act_stride, st);
+    if (rc != NDL_ERR_UNSUPPORTED) return rc;
+    const int rc2 = ndl_fake_a8_rows(mode, x, aux, nullptr, rows, n, tmp, st);
+    return rc2 != NDL_OK ? rc2 : cq_prepare(s, tmp, rows, n, bits, st);
+}
 // Matrices of one width over the current Prepare in as few launches as
 // their bits allow (the layer's projections share one activation Prepare).
 int cq_matmuls(const N3State *s, int tokens, const CqView *const *views, const CqMatmulJob *jobs, int n,
@@ -465,8 +476,7 @@ int forward_wave(N3State *s, const int32_t *tokens, const int32_t *slots, const 
     for (int l = 0; l < s->layers; l++) {
         const LayerView &L = s->layer[l];
         // hyper-connection prepare, phi matmuls, gates, Mix4, Sinkhorn
-        N3_TRY(ndl_fake_a8_rows(0, s->stream, nullptr, nullptr, R, sw, s->norm4, st));
-        N3_TRY(cq_prepare(s, s->norm4, R, sw, s->phi_pre.bits, st));
+        N3_TRY(fake_a8_prepare(s, 0, s->stream, nullptr, R, sw, s->phi_pre.bits, s->norm4, st));
         // the layer's row slices of the phi matrices, into columns [4l, 4l + 4) / [16l, 16l + 16)
         {
             const CqView *views[3] = {&s->phi_pre, &s->phi_post, &s->phi_res};
@@ -495,8 +505,7 @@ int forward_wave(N3State *s, const int32_t *tokens, const int32_t *slots, const 
             NDL_CUDA(cudaMemcpyAsync(cur, nxt, (size_t)s->slots * kEngramHistory * d * 4, cudaMemcpyDeviceToDevice, st));
         }
         // attention: prepare, projections, convs, per-head norms / RoPE / quantize, attention, gate, out, post-norm
-        N3_TRY(ndl_fake_a8_rows(1, s->residual, L.norm_in, nullptr, R, d, s->norm4, st));
-        N3_TRY(cq_prepare(s, s->norm4, R, d, L.q.bits, st));
+        N3_TRY(fake_a8_prepare(s, 1, s->residual, L.norm_in, R, d, L.q.bits, s->norm4, st));
         {
             const CqView *views[4] = {&L.q, &L.k, &L.v, &L.gate};
             const CqMatmulJob jobs[4] = {cq_job(L.q, 0, s->qw, s->q, s->qw), cq_job(L.k, 0, s->kw, s->k, s->kw),
@@ -539,8 +548,7 @@ int forward_wave(N3State *s, const int32_t *tokens, const int32_t *slots, const 
                           L.window, inv_sqrt, s->keys, s->kscale, s->values, s->vscale, s->attn_out);
             N3_TRY(check_launch("n3_attention"));
         }
-        N3_TRY(ndl_fake_a8_rows(2, s->attn_out, s->gate, nullptr, R, s->ow, s->norm4, st));
-        N3_TRY(cq_prepare(s, s->norm4, R, s->ow, L.out.bits, st));
+        N3_TRY(fake_a8_prepare(s, 2, s->attn_out, s->gate, R, s->ow, L.out.bits, s->norm4, st));
         N3_TRY(cq_matmul(L.out, s, R, 0, d, s->proj, d, st));
         // PostNormAdd(residual, proj, post_norm, sigmoid(attn_gate)): the layer's gate for every row
         N3_TRY(ndl_fake_a8_rows(3, s->proj, L.post_norm, s->gate_rows + (size_t)l * s->max_rows, R, d, s->residual,
@@ -557,8 +565,7 @@ int forward_wave(N3State *s, const int32_t *tokens, const int32_t *slots, const 
                       st, (const float *)s->stream, kLanes * d, head_rows, heads, s->headn);
         N3_TRY(check_launch("n3_pick_rows"));
         N3_TRY(ndl_hc_mix4(s->headn, d, s->quarters, heads, s->mean, st));
-        N3_TRY(ndl_fake_a8_rows(1, s->mean, s->final_norm, nullptr, heads, d, s->headn, st));
-        N3_TRY(cq_prepare(s, s->headn, heads, d, s->embedding.bits, st));
+        N3_TRY(fake_a8_prepare(s, 1, s->mean, s->final_norm, heads, d, s->embedding.bits, s->headn, st));
         N3_TRY(cq_matmul(s->embedding, s, heads, 0, s->embedding.rows, logits, s->embedding.rows, st));
     }
     return NDL_OK;

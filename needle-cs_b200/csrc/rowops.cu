@@ -15,6 +15,7 @@
 // of squares in ascending order on one lane), so every result except those
 // through exp equals the scalar restatement bit for bit.
 #include "common.cuh"
+#include "cq.cuh"
 #include "kernels.cuh"
 
 namespace ndl {
@@ -158,7 +159,10 @@ __global__ void __launch_bounds__(256) fake_a8_kernel(const float *__restrict__ 
 // row stays in registers (float4 i on thread i % 128), the squares go through
 // shared memory and thread 0 sums them in ascending order with its next four
 // float4 loads issued ahead of the current adds (the add chain is the
-// kernel's critical path); the peak is a max over the CTA.
+// kernel's critical path); the peak is a max over the CTA.  With kPrep the
+// rows go on into CQ Prepare (n % 128 == 0): warp w holds group w + 4 i of
+// the row as four consecutive elements per lane, and the prepared values,
+// scales and offsets are written instead of dst.
 constexpr int kFakeThreads = 128;
 constexpr int kFakeMaxVec = 8;
 
@@ -168,11 +172,17 @@ __device__ __forceinline__ float fake_warp_max(float v) {
     return v;
 }
 
-template <int MODE>
+struct CqPrepOut {
+    int8_t *values;
+    float *scales, *offsets;
+    int stride, bits;
+};
+
+template <int MODE, bool kPrep = false>
 __global__ void __launch_bounds__(kFakeThreads) fake_a8_row_kernel(const float *__restrict__ x,
                                                                    const float *__restrict__ aux,
                                                                    const float *__restrict__ gate, int n,
-                                                                   float *__restrict__ dst) {
+                                                                   float *__restrict__ dst, CqPrepOut prep) {
     pdl_enter();
     __shared__ float red[kFakeThreads / 32];
     __shared__ float4 squares[MODE == 2 ? 1 : kFakeThreads * kFakeMaxVec];
@@ -268,11 +278,10 @@ __global__ void __launch_bounds__(kFakeThreads) fake_a8_row_kernel(const float *
     peak = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
     const float scale = peak > 0.0f ? __fdiv_rn(peak, 127.0f) : 1.0f;
     const float round = __fdiv_rn(1.0f, scale);
-    float4 *dv = reinterpret_cast<float4 *>(dst + (size_t)row * n);
 #pragma unroll
     for (int i = 0; i < kFakeMaxVec; i++) {
         const int idx = tid + i * kFakeThreads;
-        if (idx < nv) {
+        if (idx < nv) {  // warp-uniform when kPrep (nv % 32 == 0)
             float *e = reinterpret_cast<float *>(&v[i]);
 #pragma unroll
             for (int k = 0; k < 4; k++) {
@@ -280,7 +289,15 @@ __global__ void __launch_bounds__(kFakeThreads) fake_a8_row_kernel(const float *
                 const float r = __fsub_rn(__fadd_rn(__fmul_rn(e[k], round), 12582912.0f), 12582912.0f);
                 e[k] = __fmul_rn(fminf(fmaxf(r, -128.0f), 127.0f), scale);
             }
-            dv[idx] = v[i];
+            if (kPrep) {
+                float w[4] = {e[0], e[1], e[2], e[3]};
+                const int g = idx >> 5;
+                cq_prepare_group_lane4(w, lane, prep.bits, prep.values + (size_t)row * n + (size_t)g * 128,
+                                       prep.scales + (size_t)row * prep.stride + g,
+                                       prep.offsets + (size_t)row * prep.stride + g);
+            } else {
+                reinterpret_cast<float4 *>(dst + (size_t)row * n)[idx] = v[i];
+            }
         }
     }
 }
@@ -521,6 +538,7 @@ __device__ void mlp_kron(const float *z, int active_rows, const float *left, con
             kq[q] = e / cols;
             cq[q] = e - kq[q] * cols;
         }
+#pragma unroll 4
         for (int i = 0; i < active_rows; i++)
 #pragma unroll
             for (int q = 0; q < 4; q++) sum[q] = __fadd_rn(sum[q], __fmul_rn(left[i * rows + kq[q]], z[i * cols + cq[q]]));
@@ -538,6 +556,7 @@ __device__ void mlp_kron(const float *z, int active_rows, const float *left, con
             kq[q] = e / cols;
             cq[q] = e - kq[q] * cols;
         }
+#pragma unroll 4
         for (int j = 0; j < cols; j++)
 #pragma unroll
             for (int q = 0; q < 4; q++) sum[q] = __fadd_rn(sum[q], __fmul_rn(tmp[kq[q] * cols + j], right[j * cols + cq[q]]));
@@ -549,10 +568,13 @@ __device__ void mlp_kron(const float *z, int active_rows, const float *left, con
 }
 
 // Shared floats of slot_hadamard_mlp_kernel: weights[8], normalized[dim],
-// front / back / tmp [width] and scratch[8 * dim] (squares, then the
-// ConditionWeights products).
-__host__ __device__ inline size_t mlp_smem_floats(int dim, int width) {
-    return 8 + (size_t)dim + 3 * (size_t)width + 8 * (size_t)dim;
+// front / back / tmp [width], scratch[8 * dim] (squares, then the
+// ConditionWeights products) and the six Kronecker factors (the first left
+// factor's in_rows x rows, two more rows x rows, three cols x cols).
+__host__ __device__ inline size_t mlp_smem_floats(int dim, int rows, int cols) {
+    const size_t in_rows = (size_t)(dim + cols - 1) / cols;
+    return 8 + (size_t)dim + 3 * (size_t)rows * cols + 8 * (size_t)dim + (in_rows + 2 * (size_t)rows) * rows +
+           3 * (size_t)cols * cols;
 }
 
 __global__ void __launch_bounds__(256) slot_hadamard_mlp_kernel(KtMlpArgs a) {
@@ -563,6 +585,16 @@ __global__ void __launch_bounds__(256) slot_hadamard_mlp_kernel(KtMlpArgs a) {
     const int output_rows = min(rows, (input_rows + 3) / 4 * 4);
     float *weights = sm, *normalized = sm + 8, *front = normalized + dim, *back = front + width, *tmp = back + width;
     float *scratch = tmp + width;
+    // the Kronecker factors staged once: the chains below then wait on shared memory only
+    float *left1 = scratch + 8 * dim, *right1 = left1 + input_rows * rows, *left2 = right1 + cols * cols;
+    float *right2 = left2 + rows * rows, *left3 = right2 + cols * cols, *right3 = left3 + rows * rows;
+    {
+        const int sizes[6] = {input_rows * rows, cols * cols, rows * rows, cols * cols, rows * rows, cols * cols};
+        float *dsts[6] = {left1, right1, left2, right2, left3, right3};
+#pragma unroll
+        for (int f = 0; f < 6; f++)
+            for (int i = threadIdx.x; i < sizes[f]; i += blockDim.x) dsts[f][i] = a.w[5 + f][i];
+    }
     const float *d1 = a.w[0], *d2 = a.w[1], *b2 = a.w[2], *d3 = a.w[3], *d4 = a.w[4];
     // ZeroCenteredRms: the squares in parallel, their sum in order on thread 0
     for (int i = threadIdx.x; i < dim; i += blockDim.x) {
@@ -603,7 +635,7 @@ __global__ void __launch_bounds__(256) slot_hadamard_mlp_kernel(KtMlpArgs a) {
     for (int i = threadIdx.x; i < input_rows * cols; i += blockDim.x)
         front[i] = i < dim ? __fmul_rn(normalized[i], d1[i]) : 0.0f;
     __syncthreads();
-    mlp_kron(front, input_rows, a.w[5], a.w[6], rows, cols, rows, tmp, back);
+    mlp_kron(front, input_rows, left1, right1, rows, cols, rows, tmp, back);
     for (int n = threadIdx.x; n < width; n += blockDim.x) {
         float condition = 1.0f;
         for (int j = 0; j < 8; j++) condition = __fadd_rn(condition, __fmul_rn(weights[j], a.w[12][j * width + n]));
@@ -611,16 +643,16 @@ __global__ void __launch_bounds__(256) slot_hadamard_mlp_kernel(KtMlpArgs a) {
         front[n] = __fmul_rn(v, sigmoid_rn(v));
     }
     __syncthreads();
-    mlp_kron(front, rows, a.w[7], a.w[8], rows, cols, rows, tmp, back);
+    mlp_kron(front, rows, left2, right2, rows, cols, rows, tmp, back);
     for (int n = threadIdx.x; n < width; n += blockDim.x) front[n] = __fmul_rn(back[a.perm_b[n]], d3[n]);
     __syncthreads();
-    mlp_kron(front, rows, a.w[9], a.w[10], rows, cols, output_rows, tmp, back);
+    mlp_kron(front, rows, left3, right3, rows, cols, output_rows, tmp, back);
     for (int i = threadIdx.x; i < dim; i += blockDim.x)
         residual[i] = __fadd_rn(residual[i], __fmul_rn(a.scale, __fmul_rn(back[i], d4[i])));
 }
 
 int launch_slot_hadamard_mlp(const KtMlpArgs &a, cudaStream_t stream) {
-    const size_t smem = mlp_smem_floats(a.dim, a.rows * a.cols) * 4;
+    const size_t smem = mlp_smem_floats(a.dim, a.rows, a.cols) * 4;
     if (smem > 200 * 1024) return set_error(NDL_ERR_UNSUPPORTED, "hadamard_mlp: dim %d x width %d too large", a.dim,
                                             a.rows * a.cols);
     cudaFuncSetAttribute(slot_hadamard_mlp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -665,11 +697,12 @@ int launch_fake_a8(int mode, const float *x, const float *aux, const float *gate
     if (n % 4 == 0 && n <= 4 * kFakeThreads * kFakeMaxVec && aligned(x, 16) && aligned(dst, 16) &&
         (mode == 0 || aligned(aux, 16))) {
         const dim3 grid((unsigned)rows), block(kFakeThreads);
+        const CqPrepOut none{};
         switch (mode) {
-            case 0: launch_kernel(fake_a8_row_kernel<0>, grid, block, 0, stream, x, aux, gate, n, dst); break;
-            case 1: launch_kernel(fake_a8_row_kernel<1>, grid, block, 0, stream, x, aux, gate, n, dst); break;
-            case 2: launch_kernel(fake_a8_row_kernel<2>, grid, block, 0, stream, x, aux, gate, n, dst); break;
-            default: launch_kernel(fake_a8_row_kernel<3>, grid, block, 0, stream, x, aux, gate, n, dst); break;
+            case 0: launch_kernel(fake_a8_row_kernel<0>, grid, block, 0, stream, x, aux, gate, n, dst, none); break;
+            case 1: launch_kernel(fake_a8_row_kernel<1>, grid, block, 0, stream, x, aux, gate, n, dst, none); break;
+            case 2: launch_kernel(fake_a8_row_kernel<2>, grid, block, 0, stream, x, aux, gate, n, dst, none); break;
+            default: launch_kernel(fake_a8_row_kernel<3>, grid, block, 0, stream, x, aux, gate, n, dst, none); break;
         }
         return check_launch("fake_a8_row");
     }
@@ -681,6 +714,22 @@ int launch_fake_a8(int mode, const float *x, const float *aux, const float *gate
         default: launch_kernel(fake_a8_kernel<3>, grid, block, 0, stream, x, aux, gate, rows, n, dst); break;
     }
     return check_launch("fake_a8");
+}
+
+int launch_fake_a8_prepare(int mode, const float *x, const float *aux, int rows, int n, int bits, int8_t *values,
+                           float *scales, float *offsets, int stride, cudaStream_t stream) {
+    if (mode < 0 || mode > 2 || n % 128 != 0 || n > 4 * kFakeThreads * kFakeMaxVec || !aligned(x, 16) ||
+        (mode != 0 && !aligned(aux, 16)) || stride < n / 128)
+        return NDL_ERR_UNSUPPORTED;
+    if (rows == 0) return NDL_OK;
+    const dim3 grid((unsigned)rows), block(kFakeThreads);
+    const CqPrepOut prep{values, scales, offsets, stride, bits};
+    switch (mode) {
+        case 0: launch_kernel(fake_a8_row_kernel<0, true>, grid, block, 0, stream, x, aux, nullptr, n, nullptr, prep); break;
+        case 1: launch_kernel(fake_a8_row_kernel<1, true>, grid, block, 0, stream, x, aux, nullptr, n, nullptr, prep); break;
+        default: launch_kernel(fake_a8_row_kernel<2, true>, grid, block, 0, stream, x, aux, nullptr, n, nullptr, prep); break;
+    }
+    return check_launch("fake_a8_prepare");
 }
 
 }  // namespace ndl
@@ -780,7 +829,7 @@ extern "C" NDL_API int ndl_mlp_apply(const ndl_model *m, int layer, float *resid
     a.scale = scale;
     a.residual = residual;
     a.row_stride = dim;
-    const size_t smem = mlp_smem_floats(dim, width) * 4;
+    const size_t smem = mlp_smem_floats(dim, rows, cols) * 4;
     if (smem > 200 * 1024) return set_error(NDL_ERR_UNSUPPORTED, "hadamard_mlp: dim %d x width %d too large", dim, width);
     NDL_CUDA(cudaFuncSetAttribute(slot_hadamard_mlp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     slot_hadamard_mlp_kernel<<<(unsigned)count, 256, smem, (cudaStream_t)stream>>>(a);
