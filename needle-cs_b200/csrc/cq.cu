@@ -23,7 +23,8 @@ namespace ndl {
 constexpr int kCqMaxTokens = 16;                          // tokens per matmul launch (lane t folds token t)
 constexpr int kCqWarps = 8;
 constexpr int kCqMaxCols = 8192;
-constexpr int kCqSplitMaxWarps = 8;  // warps per CTA of cq_matmul_split_kernel at most
+constexpr int kCqSplitMaxWarps = 8;   // warps per CTA of cq_matmul_split_kernel at most
+constexpr int kCqSplitMaxBlocks = 8;  // 8-token blocks per CTA of cq_matmul_split_kernel at most
 constexpr int kCqMaxJobs = 4;     // matrices per cq_matmul_split_kernel launch
 
 // Scalar.Hadamard's butterflies (src/Needle/Scalar.cs:76-89) on a warp's
@@ -347,26 +348,27 @@ struct CqJobList {
 };
 
 // The same MatMulRows for many tokens or few rows.  A CTA takes one 16-row
-// tile of one job and `tbs` 8-token blocks; its warps are (token block,
-// group phase) pairs, `split` phases per block, so warp (b, p) takes groups
-// p, p + split, ... of block b.  Per group: the A fragments as in
-// cq_matmul_kernel, the B fragments loaded straight from the prepared values
-// (each lane's eight words g*128 + 4*tig + 16*j of its token; for 2-bit the
-// plane permutation of cq_matmul_kernel's staging done with byte permutes),
-// four mma.sync, and the exact int32 dots left in shared memory with the
-// rows' norm * byte_scale and the tokens' scales and offsets.  Then each
-// (row, token) is folded over the groups in ascending order with the same
-// fp32 steps as cq_matmul_kernel (Scalar.MatMulRows,
-// src/Needle/Scalar.cs:146-192).
+// tile of one job and up to eight 8-token blocks; its warps are `split`
+// group phases times `wb` block phases: warp (p, q) takes groups p, p +
+// split, ... and, for each, blocks q, q + wb, ...  Per group the codebook
+// bytes are decoded into A fragments once (as in cq_matmul_kernel) and used
+// for every block the warp takes; per block the B fragments are loaded
+// straight from the prepared values (each lane's eight words g*128 + 4*tig +
+// 16*j of its token; for 2-bit the plane permutation of cq_matmul_kernel's
+// staging done with byte permutes), four mma.sync give the exact int32 dots,
+// which go to shared memory with the rows' norm * byte_scale and the tokens'
+// scales and offsets.  Then each (row, token) is folded over the groups in
+// ascending order with the same fp32 steps as cq_matmul_kernel
+// (Scalar.MatMulRows, src/Needle/Scalar.cs:146-192).
 template <int kBits>
 __global__ void __launch_bounds__(32 * kCqSplitMaxWarps) cq_matmul_split_kernel(
     CqJobList jobs, int cols, const int8_t *__restrict__ values, const float *__restrict__ scales,
-    const float *__restrict__ offsets, int stride, int tokens, int split) {
+    const float *__restrict__ offsets, int stride, int tokens, int split, int tbs) {
     extern __shared__ __align__(16) uint8_t smem[];
     const int groups = cols / 128, row_words = cols * kBits / 32;
     constexpr int kGroupWords = kBits == 2 ? 8 : 16;
     constexpr int kBlocks = kBits == 2 ? 1 : 2;
-    const int tbs = (int)(blockDim.x >> 5) / split, token_blocks = (tokens + 7) >> 3;
+    const int wb = (int)(blockDim.x >> 5) / split, token_blocks = (tokens + 7) >> 3;
     const int ctas_per_tile = (token_blocks + tbs - 1) / tbs;
     const int tile = blockIdx.x / ctas_per_tile, tb0 = (blockIdx.x - tile * ctas_per_tile) * tbs;
     CqJob job = jobs.job[0];
@@ -375,29 +377,22 @@ __global__ void __launch_bounds__(32 * kCqSplitMaxWarps) cq_matmul_split_kernel(
         if (i < jobs.n && tile >= jobs.job[i].tile_begin) job = jobs.job[i];
     const int r_base = job.row_start + (tile - job.tile_begin) * 16;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
-    const int tl = warp / split, phase = warp - tl * split;
+    const int bq = warp / split, phase = warp - bq * split;
     int *dots = reinterpret_cast<int *>(smem);                         // [tbs][groups][16 rows][8 tokens]
     float *nf = reinterpret_cast<float *>(dots + tbs * groups * 128);  // [groups][16]
     float *ss = nf + groups * 16;                                      // [tbs][groups][8]
     float *os = ss + tbs * groups * 8;                                 // [tbs][groups][8]
-    const int r0 = r_base + gid, r1 = r0 + 8, t = (tb0 + tl) * 8 + gid;
-    const bool ok0 = r0 < job.row_end, ok1 = r1 < job.row_end, okt = t < tokens;
+    const int r0 = r_base + gid, r1 = r0 + 8;
+    const bool ok0 = r0 < job.row_end, ok1 = r1 < job.row_end;
     const uint32_t *w0 = job.indices + (size_t)(ok0 ? r0 : job.row_start) * row_words;
     const uint32_t *w1 = job.indices + (size_t)(ok1 ? r1 : job.row_start) * row_words;
-    const uint32_t *xw = reinterpret_cast<const uint32_t *>(values + (size_t)(okt ? t : 0) * cols) + tig;
-    // one side value per lane and group: lanes 0..15 a row's norm * byte_scale
-    // (written by the first block's warps), 16..23 a token's scale, 24..31 its offset
-    const int side_row = r_base + (lane & 15), side_tok = (tb0 + tl) * 8 + (lane & 7);
-    const bool side_ok = lane < 16 ? side_row < job.row_end : side_tok < tokens;
-    const bool side_writes = lane >= 16 || tl == 0;
+    // side values per lane: lanes 0..15 a row's norm * byte_scale (block phase 0
+    // writes them), 16..23 a token's scale, 24..31 its offset
+    const int side_row = r_base + (lane & 15);
     const float *side_src = lane < 24 ? scales : offsets;
-    float *side_dst = lane < 16 ? nf + lane : (lane < 24 ? ss : os) + (size_t)tl * groups * 8 + (lane & 7);
-    const int side_step = lane < 16 ? 16 : 8;
-    int *my_dots = dots + (size_t)tl * groups * 128;
     pdl_enter();
-#pragma unroll 2
     for (int g = phase; g < groups; g += split) {
-        uint32_t c0[kBlocks][2], c1[kBlocks][2], x[8];
+        uint32_t c0[kBlocks][2], c1[kBlocks][2];
 #pragma unroll
         for (int h = 0; h < kBlocks; h++) {
             const int wi = g * kGroupWords + 8 * h + tig;
@@ -406,43 +401,62 @@ __global__ void __launch_bounds__(32 * kCqSplitMaxWarps) cq_matmul_split_kernel(
             c1[h][0] = ok1 ? __ldg(w1 + wi) : 0u;
             c1[h][1] = ok1 ? __ldg(w1 + wi + 4) : 0u;
         }
-#pragma unroll
-        for (int j = 0; j < 8; j++) x[j] = okt ? __ldg(xw + g * 32 + 4 * j) : 0u;
-        float side = 0.0f;
-        if (side_ok && side_writes)
-            side = lane < 16 ? __fmul_rn(half_to_float_ref_fast(job.norms[(size_t)side_row * groups + g]),
-                                         job.book.byte_scale)
-                             : side_src[(size_t)side_tok * stride + g];
-        int d[4] = {0, 0, 0, 0};
+        if (lane < 16 && bq == 0)
+            nf[g * 16 + lane] = side_row < job.row_end
+                                    ? __fmul_rn(half_to_float_ref_fast(job.norms[(size_t)side_row * groups + g]),
+                                                job.book.byte_scale)
+                                    : 0.0f;
+        uint32_t a[4][4];  // A fragments of MMA k
         if (kBits == 2) {
-            uint32_t dec[4][4];
             const uint32_t wds[4] = {c0[0][0], c1[0][0], c0[0][1], c1[0][1]};
+            uint32_t dec[4][4];
 #pragma unroll
             for (int j = 0; j < 4; j++) cq_decode2(wds[j], job.book.bytes[0], dec[j]);
 #pragma unroll
-            for (int k = 0; k < 4; k++) {
-                // byte i of half h of MMA k: plane (k & 1) + 2 (i & 1) of byte 2 (k >> 1) + (i >> 1), i.e.
-                // word h + 2 (k & 1) (even i) or h + 2 (k & 1) + 4 (odd i) of this lane's eight
-                const uint32_t a[4] = {dec[0][k], dec[1][k], dec[2][k], dec[3][k]};
-                const uint32_t sel = (k >> 1) ? 0x7362u : 0x5140u;
-                const int p = 2 * (k & 1);
-                cq_mma(d, a, cq_prmt(x[p], x[p + 4], sel), cq_prmt(x[p + 1], x[p + 5], sel));
-            }
+            for (int k = 0; k < 4; k++)
+#pragma unroll
+                for (int j = 0; j < 4; j++) a[k][j] = dec[j][k];
         } else {
 #pragma unroll
             for (int k = 0; k < 4; k++) {
                 const int h = k >> 1;
-                const uint32_t a[4] = {cq_lut_plane4(c0[h][0], k & 1, job.book.bytes),
-                                       cq_lut_plane4(c1[h][0], k & 1, job.book.bytes),
-                                       cq_lut_plane4(c0[h][1], k & 1, job.book.bytes),
-                                       cq_lut_plane4(c1[h][1], k & 1, job.book.bytes)};
-                cq_mma(d, a, x[2 * k], x[2 * k + 1]);
+                a[k][0] = cq_lut_plane4(c0[h][0], k & 1, job.book.bytes);
+                a[k][1] = cq_lut_plane4(c1[h][0], k & 1, job.book.bytes);
+                a[k][2] = cq_lut_plane4(c0[h][1], k & 1, job.book.bytes);
+                a[k][3] = cq_lut_plane4(c1[h][1], k & 1, job.book.bytes);
             }
         }
-        // rows gid, gid + 8; tokens 2 tig, 2 tig + 1
-        *reinterpret_cast<int2 *>(my_dots + g * 128 + gid * 8 + 2 * tig) = make_int2(d[0], d[1]);
-        *reinterpret_cast<int2 *>(my_dots + g * 128 + (gid + 8) * 8 + 2 * tig) = make_int2(d[2], d[3]);
-        if (side_writes) side_dst[g * side_step] = side;
+#pragma unroll 2
+        for (int b = bq; b < tbs; b += wb) {
+            const int t = (tb0 + b) * 8 + gid;
+            const bool okt = t < tokens;
+            const uint32_t *xw = reinterpret_cast<const uint32_t *>(values + (size_t)(okt ? t : 0) * cols) + g * 32 + tig;
+            uint32_t x[8];
+#pragma unroll
+            for (int j = 0; j < 8; j++) x[j] = okt ? __ldg(xw + 4 * j) : 0u;
+            if (lane >= 16) {
+                const int side_tok = (tb0 + b) * 8 + (lane & 7);
+                (lane < 24 ? ss : os)[((size_t)b * groups + g) * 8 + (lane & 7)] =
+                    side_tok < tokens ? side_src[(size_t)side_tok * stride + g] : 0.0f;
+            }
+            int d[4] = {0, 0, 0, 0};
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                if (kBits == 2) {
+                    // byte i of half h of MMA k: plane (k & 1) + 2 (i & 1) of byte 2 (k >> 1) + (i >> 1), i.e.
+                    // word h + 2 (k & 1) (even i) or h + 2 (k & 1) + 4 (odd i) of this lane's eight
+                    const uint32_t sel = (k >> 1) ? 0x7362u : 0x5140u;
+                    const int p = 2 * (k & 1);
+                    cq_mma(d, a[k], cq_prmt(x[p], x[p + 4], sel), cq_prmt(x[p + 1], x[p + 5], sel));
+                } else {
+                    cq_mma(d, a[k], x[2 * k], x[2 * k + 1]);
+                }
+            }
+            // rows gid, gid + 8; tokens 2 tig, 2 tig + 1
+            int *bd = dots + ((size_t)b * groups + g) * 128;
+            *reinterpret_cast<int2 *>(bd + gid * 8 + 2 * tig) = make_int2(d[0], d[1]);
+            *reinterpret_cast<int2 *>(bd + (gid + 8) * 8 + 2 * tig) = make_int2(d[2], d[3]);
+        }
     }
     __syncthreads();
     for (int q = threadIdx.x; q < tbs * 128; q += blockDim.x) {
@@ -522,13 +536,13 @@ int launch_cq_prepare(const float *x, int tokens, int cols, int bits, int8_t *va
 int launch_cq_matmul_jobs(const CqMatmulJob *jobs, int n_jobs, int cols, int bits, const int8_t *values,
                           const float *scales, const float *offsets, int stride, int tokens, cudaStream_t stream) {
     if (tokens == 0) return NDL_OK;
-    const int groups = cols / 128, token_blocks = (tokens + 7) / 8;
-    // group phases per token block: about three groups per warp; token blocks
-    // per CTA fill it up to kCqSplitMaxWarps warps
-    const int split = groups >= 24 ? 8 : groups >= 12 ? 4 : groups >= 6 ? 2 : 1;
-    const int tbs = kCqSplitMaxWarps / split < token_blocks ? kCqSplitMaxWarps / split : token_blocks;
-    const long long ctas_per_tile = (token_blocks + tbs - 1) / tbs;
-    const size_t smem = ((size_t)tbs * groups * (128 + 16) + (size_t)groups * 16) * 4;  // dots, scales, offsets, norms
+    const int groups = cols / 128, token_blocks = (tokens + 7) / 8, sms = device_sm_count();
+    // a warp per group phase (up to kCqSplitMaxWarps), the rest as block phases
+    const int split = groups < kCqSplitMaxWarps ? groups : kCqSplitMaxWarps;
+    // token blocks per CTA: within 48 KB of shared memory and kCqSplitMaxBlocks
+    int cap = (12288 - 16 * groups) / (144 * groups);
+    cap = cap < kCqSplitMaxBlocks ? cap : kCqSplitMaxBlocks;
+    cap = cap < token_blocks ? cap : token_blocks;
     int next = 0;
     while (next < n_jobs) {
         CqJobList list{};
@@ -549,14 +563,20 @@ int launch_cq_matmul_jobs(const CqMatmulJob *jobs, int n_jobs, int cols, int bit
             tiles += (s.row_end - s.row_start + 15) / 16;
         }
         if (list.n == 0) break;
-        const long long blocks = tiles * ctas_per_tile;
+        // fewer blocks per CTA (more CTAs, each block's decode repeated) while
+        // the grid would not give every SM two CTAs
+        int tbs = cap;
+        while (tbs > 1 && tiles * ((token_blocks + tbs - 1) / tbs) < 2LL * sms) tbs--;
+        const int wb = kCqSplitMaxWarps / split < tbs ? kCqSplitMaxWarps / split : tbs;
+        const long long blocks = tiles * ((token_blocks + tbs - 1) / tbs);
         if (blocks > 0x7fffffffLL) return set_error(NDL_ERR_INVALID_ARG, "cq matmul: %lld CTAs", blocks);
+        const size_t smem = ((size_t)tbs * groups * (128 + 16) + (size_t)groups * 16) * 4;  // dots, scales, offsets, norms
         if (bits == 2)
-            launch_kernel(cq_matmul_split_kernel<2>, dim3((unsigned)blocks), dim3(32 * split * tbs), smem, stream,
-                          list, cols, values, scales, offsets, stride, tokens, split);
+            launch_kernel(cq_matmul_split_kernel<2>, dim3((unsigned)blocks), dim3(32 * split * wb), smem, stream,
+                          list, cols, values, scales, offsets, stride, tokens, split, tbs);
         else
-            launch_kernel(cq_matmul_split_kernel<4>, dim3((unsigned)blocks), dim3(32 * split * tbs), smem, stream,
-                          list, cols, values, scales, offsets, stride, tokens, split);
+            launch_kernel(cq_matmul_split_kernel<4>, dim3((unsigned)blocks), dim3(32 * split * wb), smem, stream,
+                          list, cols, values, scales, offsets, stride, tokens, split, tbs);
         const int st = check_launch("cq_matmul_split");
         if (st != NDL_OK) return st;
     }

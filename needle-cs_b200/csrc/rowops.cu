@@ -569,13 +569,39 @@ __device__ void mlp_kron(const float *z, int active_rows, const float *left, con
 
 // Shared floats of slot_hadamard_mlp_kernel: weights[8], normalized[dim],
 // front / back / tmp [width], scratch[8 * dim] (squares, then the
-// ConditionWeights products) and the six Kronecker factors (the first left
-// factor's in_rows x rows, two more rows x rows, three cols x cols).
+// ConditionWeights products), the residual row [dim] and the six Kronecker
+// factors (the first left factor's in_rows x rows, two more rows x rows,
+// three cols x cols).
 __host__ __device__ inline size_t mlp_smem_floats(int dim, int rows, int cols) {
     const size_t in_rows = (size_t)(dim + cols - 1) / cols;
-    return 8 + (size_t)dim + 3 * (size_t)rows * cols + 8 * (size_t)dim + (in_rows + 2 * (size_t)rows) * rows +
+    return 8 + (size_t)dim + 3 * (size_t)rows * cols + 9 * (size_t)dim + (in_rows + 2 * (size_t)rows) * rows +
            3 * (size_t)cols * cols;
 }
+
+// Element loop over [0, n) in which every thread issues the loads of kBatch
+// of its elements (load(i), global) before it uses any of them (use(i, v)):
+// one memory round trip per kBatch elements instead of one per element.
+template <int kBatch, typename Load, typename Use>
+__device__ __forceinline__ void mlp_batched(int n, int tid, int threads, Load load, Use use) {
+    for (int base = tid; base < n; base += kBatch * threads) {
+        decltype(load(0)) v[kBatch];
+#pragma unroll
+        for (int k = 0; k < kBatch; k++) {
+            const int i = base + k * threads;
+            if (i < n) v[k] = load(i);
+        }
+#pragma unroll
+        for (int k = 0; k < kBatch; k++) {
+            const int i = base + k * threads;
+            if (i < n) use(i, v[k]);
+        }
+    }
+}
+
+struct MlpCondition {
+    float w[8], d2, b2;
+    int perm;
+};
 
 __global__ void __launch_bounds__(256) slot_hadamard_mlp_kernel(KtMlpArgs a) {
     extern __shared__ float sm[];
@@ -583,47 +609,55 @@ __global__ void __launch_bounds__(256) slot_hadamard_mlp_kernel(KtMlpArgs a) {
     const int dim = a.dim, rows = a.rows, cols = a.cols, width = rows * cols;
     const int input_rows = (dim + cols - 1) / cols;
     const int output_rows = min(rows, (input_rows + 3) / 4 * 4);
+    const int tid = threadIdx.x, nt = blockDim.x;
     float *weights = sm, *normalized = sm + 8, *front = normalized + dim, *back = front + width, *tmp = back + width;
-    float *scratch = tmp + width;
-    // the Kronecker factors staged once: the chains below then wait on shared memory only
-    float *left1 = scratch + 8 * dim, *right1 = left1 + input_rows * rows, *left2 = right1 + cols * cols;
+    float *scratch = tmp + width, *res = scratch + 8 * dim;
+    float *left1 = res + dim, *right1 = left1 + input_rows * rows, *left2 = right1 + cols * cols;
     float *right2 = left2 + rows * rows, *left3 = right2 + cols * cols, *right3 = left3 + rows * rows;
-    {
-        const int sizes[6] = {input_rows * rows, cols * cols, rows * rows, cols * cols, rows * rows, cols * cols};
-        float *dsts[6] = {left1, right1, left2, right2, left3, right3};
-#pragma unroll
-        for (int f = 0; f < 6; f++)
-            for (int i = threadIdx.x; i < sizes[f]; i += blockDim.x) dsts[f][i] = a.w[5 + f][i];
-    }
-    const float *d1 = a.w[0], *d2 = a.w[1], *b2 = a.w[2], *d3 = a.w[3], *d4 = a.w[4];
-    // ZeroCenteredRms: the squares in parallel, their sum in order on thread 0
-    for (int i = threadIdx.x; i < dim; i += blockDim.x) {
-        const float r = residual[i];
+    const float *__restrict__ d1 = a.w[0], *__restrict__ d2 = a.w[1], *__restrict__ b2 = a.w[2];
+    const float *__restrict__ d3 = a.w[3], *__restrict__ d4 = a.w[4], *__restrict__ cond_v = a.w[11];
+    const float *__restrict__ cond_u = a.w[12], *__restrict__ pre = a.pre_norm;
+    const int32_t *__restrict__ perm_a = a.perm_a, *__restrict__ perm_b = a.perm_b;
+    // the residual row and its squares (ZeroCenteredRms)
+    mlp_batched<4>(dim, tid, nt, [&](int i) { return residual[i]; }, [&](int i, float r) {
+        res[i] = r;
         scratch[i] = __fmul_rn(r, r);
-    }
+    });
     __syncthreads();
-    if (threadIdx.x == 0) {
+    if (tid == 0) {  // the sum of squares in order
         float sum = 0.0f;
 #pragma unroll 16
         for (int i = 0; i < dim; i++) sum = __fadd_rn(sum, scratch[i]);
         weights[0] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, (float)dim), 1e-6f)));
+    } else if (tid >= 32) {  // meanwhile the other warps stage the Kronecker factors
+        const int sizes[6] = {input_rows * rows, cols * cols, rows * rows, cols * cols, rows * rows, cols * cols};
+        float *dsts[6] = {left1, right1, left2, right2, left3, right3};
+#pragma unroll
+        for (int f = 0; f < 6; f++) {
+            const float *__restrict__ src = a.w[5 + f];
+            float *dst = dsts[f];
+            mlp_batched<8>(sizes[f], tid - 32, nt - 32, [&](int i) { return __ldg(src + i); },
+                           [&](int i, float v) { dst[i] = v; });
+        }
     }
     __syncthreads();
     const float inv = weights[0];
-    for (int i = threadIdx.x; i < dim; i += blockDim.x)
-        normalized[i] = __fmul_rn(__fmul_rn(__fadd_rn(1.0f, a.pre_norm[i]), residual[i]), inv);
+    mlp_batched<4>(dim, tid, nt, [&](int i) { return __ldg(pre + i); }, [&](int i, float p) {
+        normalized[i] = __fmul_rn(__fmul_rn(__fadd_rn(1.0f, p), res[i]), inv);
+    });
     __syncthreads();
     // ConditionWeights: products in parallel, weight j summed in order by thread j
-    for (int e = threadIdx.x; e < dim * 8; e += blockDim.x) scratch[e] = __fmul_rn(normalized[e >> 3], a.w[11][e]);
+    mlp_batched<8>(dim * 8, tid, nt, [&](int e) { return __ldg(cond_v + e); },
+                   [&](int e, float w) { scratch[e] = __fmul_rn(normalized[e >> 3], w); });
     __syncthreads();
-    if (threadIdx.x < 8) {
+    if (tid < 8) {
         float sum = 0.0f;
 #pragma unroll 16
-        for (int i = 0; i < dim; i++) sum = __fadd_rn(sum, scratch[i * 8 + threadIdx.x]);
-        weights[threadIdx.x] = sum;
+        for (int i = 0; i < dim; i++) sum = __fadd_rn(sum, scratch[i * 8 + tid]);
+        weights[tid] = sum;
     }
     __syncthreads();
-    if (threadIdx.x == 0) {  // Softmax over the 8 weights
+    if (tid == 0) {  // Softmax over the 8 weights
         float peak = -INFINITY, total = 0.0f;
         for (int j = 0; j < 8; j++) peak = fmaxf(peak, weights[j]);
         for (int j = 0; j < 8; j++) {
@@ -632,23 +666,36 @@ __global__ void __launch_bounds__(256) slot_hadamard_mlp_kernel(KtMlpArgs a) {
         }
         for (int j = 0; j < 8; j++) weights[j] = __fdiv_rn(weights[j], total);
     }
-    for (int i = threadIdx.x; i < input_rows * cols; i += blockDim.x)
-        front[i] = i < dim ? __fmul_rn(normalized[i], d1[i]) : 0.0f;
+    mlp_batched<4>(input_rows * cols, tid, nt, [&](int i) { return i < dim ? __ldg(d1 + i) : 0.0f; },
+                   [&](int i, float w) { front[i] = i < dim ? __fmul_rn(normalized[i], w) : 0.0f; });
     __syncthreads();
     mlp_kron(front, input_rows, left1, right1, rows, cols, rows, tmp, back);
-    for (int n = threadIdx.x; n < width; n += blockDim.x) {
-        float condition = 1.0f;
-        for (int j = 0; j < 8; j++) condition = __fadd_rn(condition, __fmul_rn(weights[j], a.w[12][j * width + n]));
-        const float v = __fadd_rn(__fmul_rn(__fmul_rn(d2[n], condition), back[a.perm_a[n]]), b2[n]);
-        front[n] = __fmul_rn(v, sigmoid_rn(v));
-    }
+    mlp_batched<4>(width, tid, nt,
+                   [&](int n) {
+                       MlpCondition c;
+#pragma unroll
+                       for (int j = 0; j < 8; j++) c.w[j] = __ldg(cond_u + j * width + n);
+                       c.d2 = __ldg(d2 + n);
+                       c.b2 = __ldg(b2 + n);
+                       c.perm = __ldg(perm_a + n);
+                       return c;
+                   },
+                   [&](int n, const MlpCondition &c) {
+                       float condition = 1.0f;
+#pragma unroll
+                       for (int j = 0; j < 8; j++) condition = __fadd_rn(condition, __fmul_rn(weights[j], c.w[j]));
+                       const float v = __fadd_rn(__fmul_rn(__fmul_rn(c.d2, condition), back[c.perm]), c.b2);
+                       front[n] = __fmul_rn(v, sigmoid_rn(v));
+                   });
     __syncthreads();
     mlp_kron(front, rows, left2, right2, rows, cols, rows, tmp, back);
-    for (int n = threadIdx.x; n < width; n += blockDim.x) front[n] = __fmul_rn(back[a.perm_b[n]], d3[n]);
+    mlp_batched<4>(width, tid, nt, [&](int n) { return make_float2(__int_as_float(__ldg(perm_b + n)), __ldg(d3 + n)); },
+                   [&](int n, float2 p) { front[n] = __fmul_rn(back[__float_as_int(p.x)], p.y); });
     __syncthreads();
     mlp_kron(front, rows, left3, right3, rows, cols, output_rows, tmp, back);
-    for (int i = threadIdx.x; i < dim; i += blockDim.x)
-        residual[i] = __fadd_rn(residual[i], __fmul_rn(a.scale, __fmul_rn(back[i], d4[i])));
+    mlp_batched<4>(dim, tid, nt, [&](int i) { return __ldg(d4 + i); }, [&](int i, float w) {
+        residual[i] = __fadd_rn(res[i], __fmul_rn(a.scale, __fmul_rn(back[i], w)));
+    });
 }
 
 int launch_slot_hadamard_mlp(const KtMlpArgs &a, cudaStream_t stream) {
