@@ -1039,14 +1039,18 @@ NEEDLE3_SHAPE = dict(dim=768, heads=12, kv_heads=2, layers=20, vocab=8192, hada_
                      global_mask=sum(1 << l for l in range(3, 20, 4)), max_seq=512)
 
 
-def needle3_archive(seed):
+def needle3_archive(seed, layers=None):
     """A synthetic archive of Needle 3's shape (20 layers, d 768, 12 query heads over 2 kv heads of 48 / 64
     dims, vocab 8192, the Kronecker MLP over HadaN 1024, Engram sites at layers 1 and 10; CQ weights with
-    random codes), written by the test suite's archive writer."""
+    random codes), written by the test suite's archive writer.  `layers` < 20 keeps the first layers (one
+    Engram site, at layer 1; the last layer global) for small profiling runs."""
     sys.path.insert(0, os.path.join(ROOT, "tests"))
     from cact_support import needle3_decoder_archive
 
-    return needle3_decoder_archive(seed=seed, **NEEDLE3_SHAPE)
+    shape = dict(NEEDLE3_SHAPE)
+    if layers is not None and layers < shape["layers"]:
+        shape.update(layers=layers, sites=[1], global_mask=1 << (layers - 1))
+    return needle3_decoder_archive(seed=seed, **shape)
 
 
 def run_needle3(args, rank, world, local):
@@ -1065,7 +1069,7 @@ def run_needle3(args, rank, world, local):
     torch.cuda.set_device(device)
     cact = __import__("needle_cs_b200.model", fromlist=["model"])
     eng_mod = __import__("needle_cs_b200.engine", fromlist=["engine"])
-    a = needle3_archive(seed=5)
+    a = needle3_archive(seed=5, layers=args.layers)
     data = a.build()
     m = cact.Model(data, device=local)
     g = m.info
@@ -1116,13 +1120,14 @@ def run_needle3(args, rank, world, local):
                                             "sites": list(g["sites"][:g["site_count"]]), "sessions_per_gpu": B,
                                             "prompt": P, "greedy": True, "weight_bytes": weights,
                                             "l2": "weights fit L2; each step reads them and every session's cache"},
-            "roofline": {"bound": "hbm", "kernel": "the whole step (launch- and latency-bound: ~27 kernels per layer "
+            "roofline": {"bound": "hbm", "kernel": "the whole step (launch- and latency-bound: 18 kernels per layer "
                                                    "on 64 rows, replayed from a CUDA graph)",
                          "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak, "traffic": None,
                          "peak_source": peak_source, "algorithmic_bytes_per_step": step_bytes},
             "e2e": {"value": world * B * args.steps / wall, "unit": "tokens/s", "h2d_bytes_per_step": B * 12,
                     "d2h_bytes_per_step": B * 4},
-            "gpu_launches": args.steps * (L * 27 + 8), "clocks": clocks.summary()}
+            # per step: 18 kernels a layer, 8 more at each Engram site, embedding 2, head 5, argmax 1
+            "gpu_launches": args.steps * (L * 18 + 8 * g["site_count"] + 8), "clocks": clocks.summary()}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         entry.load_oracle()
         line["cpu_baseline"] = needle3_cpu_sample(a)
@@ -1467,6 +1472,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="cfg5")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=None,
+                    help="needle3 only: fewer layers than Needle 3's 20 (a small case for ncu captures)")
     ap.add_argument("--case", nargs="+", metavar="CASE",
                     help="run a profiling case instead: attention | gemm M N K")
     args = ap.parse_args()
