@@ -772,6 +772,47 @@ NDL_API int ndl_model_read_host(const ndl_model *m, const char *role, int index,
 /* The tokenizer record's bytes (owned by the model). */
 NDL_API int ndl_model_tokenizer(const ndl_model *m, const void **blob, size_t *bytes);
 
+/* ---- Whistle encoder ---------------------------------------------------
+ * Replaces Whistle.Encode + BuildCrossMemory (src/Needle/Whistle.cs:179-200,
+ * 886-914) for a loaded archive with an audio section (AudioWeights,
+ * src/Needle/Audio.cs:117-149), on the model's device: the log-mel front end
+ * (FeatureJob, src/Needle/Frontend.cs:82-130), Normalize, the three-stage
+ * stem, the encoder layers (RunEncoder, :794-828) and the final norm, then
+ * every decoder layer's cross memory (int8 keys and values per (frame,
+ * head) with fp32 scales, the layout of CrossMemory).  The scalar tier
+ * throughout, with MathF.Exp and MathF.Log as the correctly rounded
+ * functions, so every output equals the scalar chain bit for bit.
+ * create: max_samples bounds the PCM per call (at most the reference's 30 s);
+ * encode: host or device PCM samples in [-1, 1] (the first 30 s kept);
+ *   *frames = encoder rows ((((samples / hop) + 1) / 2 + 1) / 2 + 1) / 2, 0
+ *   below one hop; returns when the work is done.  encode_device queues the
+ *   same work on ndl_whistle_stream without waiting (pcm device or host).
+ * read: copies a result to host memory (bytes at least its size, *written
+ *   its size): NDL_WHISTLE_MEL [mel frames][mels] after Normalize, _STEM
+ *   [frames][dim], _ENCODER [frames][dim], and of decoder layer `layer`
+ *   _KEYS int8 [frames][heads][qk], _KEY_SCALES fp32 [frames][heads],
+ *   _VALUES int8 [frames][heads][v], _VALUE_SCALES fp32 [frames][heads].
+ * NDL_ERR_UNSUPPORTED for an archive without audio or a geometry the device
+ * encoder does not take (CQ widths not in 128-column groups, dim > 1024,
+ * head dims > 64, fft > 4096 or not a power of two). */
+typedef struct ndl_whistle ndl_whistle;
+enum {
+    NDL_WHISTLE_MEL = 0,
+    NDL_WHISTLE_STEM = 1,
+    NDL_WHISTLE_ENCODER = 2,
+    NDL_WHISTLE_KEYS = 3,
+    NDL_WHISTLE_KEY_SCALES = 4,
+    NDL_WHISTLE_VALUES = 5,
+    NDL_WHISTLE_VALUE_SCALES = 6
+};
+NDL_API int ndl_whistle_create(const ndl_model *m, int max_samples, ndl_whistle **out);
+NDL_API int ndl_whistle_encode(ndl_whistle *w, const float *pcm, int samples, int *frames);
+NDL_API int ndl_whistle_encode_device(ndl_whistle *w, const float *pcm, int samples);
+NDL_API int ndl_whistle_frames(const ndl_whistle *w, int *frames, int *mel_frames);
+NDL_API int ndl_whistle_read(ndl_whistle *w, int what, int layer, void *dst, size_t bytes, size_t *written);
+NDL_API void *ndl_whistle_stream(ndl_whistle *w);
+NDL_API int ndl_whistle_destroy(ndl_whistle *w);
+
 /* The Engram block of one site on a loaded model (EngineCore.ApplyEngramBatch,
  * src/Needle/Engine.cs:2405-2469), chained on `stream` over `count` tokens:
  *   rows = the n-gram hash rows (ndl_engram_hash, the model's orders, heads

@@ -43,6 +43,13 @@ SIGNATURES = {
                                             c_int, c_void_p, c_size_t, c_int, c_int, c_void_p, c_void_p, c_void_p]),
     "ndl_engine_create": (c_int, [c_void_p, c_void_p, ctypes.POINTER(c_void_p)]),
     "ndl_engine_create_model": (c_int, [c_void_p, c_void_p, ctypes.POINTER(c_void_p)]),
+    "ndl_whistle_create": (c_int, [c_void_p, c_int, ctypes.POINTER(c_void_p)]),
+    "ndl_whistle_encode": (c_int, [c_void_p, c_void_p, c_int, ctypes.POINTER(c_int)]),
+    "ndl_whistle_encode_device": (c_int, [c_void_p, c_void_p, c_int]),
+    "ndl_whistle_frames": (c_int, [c_void_p, ctypes.POINTER(c_int), ctypes.POINTER(c_int)]),
+    "ndl_whistle_read": (c_int, [c_void_p, c_int, c_int, c_void_p, c_size_t, ctypes.POINTER(c_size_t)]),
+    "ndl_whistle_stream": (c_void_p, [c_void_p]),
+    "ndl_whistle_destroy": (c_int, [c_void_p]),
     "ndl_engine_destroy": (c_int, [c_void_p]),
     "ndl_engine_stream": (c_int, [c_void_p, ctypes.POINTER(c_void_p)]),
     "ndl_engine_tensor": (c_int, [c_void_p, c_char_p, c_int, ctypes.POINTER(c_void_p), ctypes.POINTER(c_size_t)]),

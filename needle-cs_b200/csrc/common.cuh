@@ -188,6 +188,25 @@ __device__ __forceinline__ float sigmoid_rn(float x) {
 }
 #endif
 
+// exp_rn's steps on the host (MathF.Exp in double, one rounding), for the
+// sigmoids of stored gate logits that the host evaluates once per model.
+inline float host_exp_rn(float x) {
+    if (x != x) return x;
+    if (x > 89.0f) return INFINITY;
+    if (x < -104.0f) return 0.0f;
+    const double xd = (double)x;
+    const double k = rint(xd * 1.4426950408889634);
+    const double r = (xd - k * 6.93147180369123816490e-01) - k * 1.90821492927058770002e-10;
+    double p = 1.6059043836821614599e-10;
+    const double c[] = {2.0876756987868098979e-09, 2.5052108385441718775e-08, 2.7557319223985890653e-07,
+                        2.7557319223985890653e-06, 2.4801587301587301587e-05, 1.9841269841269841270e-04,
+                        1.3888888888888888889e-03, 8.3333333333333333333e-03, 4.1666666666666666667e-02,
+                        1.6666666666666666667e-01, 0.5, 1.0, 1.0};
+    for (double ci : c) p = fma(p, r, ci);
+    return (float)scalbn(p, (int)k);
+}
+inline float host_sigmoid_rn(float x) { return 1.0f / (1.0f + host_exp_rn(-x)); }
+
 // IEEE round-to-nearest-even float -> binary16 (integer-only).
 __host__ __device__ __forceinline__ uint16_t float_to_half_rne(float f) {
 #ifdef __CUDA_ARCH__

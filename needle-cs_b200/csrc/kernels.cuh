@@ -102,6 +102,13 @@ int launch_gemv_i8g32(const MatmulArgs &a, cudaStream_t stream);
 // shape does not fit its tiling so the caller can fall back to the GEMV.
 int launch_gemm_i8g32_tc(const MatmulArgs &a, cudaStream_t stream);
 
+// CQ Prepare (Quant.PrepareRange's scalar branch) and MatMulRows on one
+// matrix (ndl_cq_prepare / ndl_cq_matmul without the argument checks).
+int launch_cq_prepare(const float *x, int tokens, int cols, int bits, int8_t *values, float *scales, float *offsets,
+                      int stride, cudaStream_t stream);
+int launch_cq_matmul(const uint8_t *indices, const uint16_t *norms, const uint8_t *book_bytes, float byte_scale,
+                     int cols, int bits, const int8_t *values, const float *scales, const float *offsets, int stride,
+                     int tokens, float *y, int ldy, int row_start, int row_end, cudaStream_t stream);
 // One CQ matrix (or row slice of one) for launch_cq_matmul_jobs: rows
 // [row_start, row_end) of y [tokens][ldy] from the shared prepared
 // activations; book_bytes is the host copy of the 16 codebook bytes.
@@ -113,11 +120,32 @@ struct CqMatmulJob {
     float *y;
     int ldy, row_start, row_end;
 };
+// Where a row op writes CQ Prepare's output (values [rows][n], scales and
+// offsets [rows][stride]) instead of its rows.
+struct CqPrepOut {
+    int8_t *values;
+    float *scales, *offsets;
+    int stride, bits;
+};
+// CTA-per-row row ops (n % 4 == 0, n <= 4096, 16-byte aligned rows; n % 128
+// == 0 with prep): mode 0 RmsUnit, 1 ZeroCenteredRms (aux = scale), 2
+// MultiplyBySigmoid (aux = gate rows), 3 PostNormAdd (aux = scale, dst =
+// residual, gate[row]; fake and prep not allowed), 4 ZeroCenteredRms then
+// SiLU, 5 the row unchanged; fake adds Quant.FakeA8; prep (nullable) sends
+// the rows into CQ Prepare instead of dst.  NDL_ERR_UNSUPPORTED (nothing
+// launched) for a shape or alignment the kernel does not take.
+int launch_row_op(int mode, bool fake, const float *x, const float *aux, const float *gate, int rows, int n,
+                  float *dst, const CqPrepOut *prep, cudaStream_t stream);
 // ndl_fake_a8_rows modes 0..2 followed by CQ Prepare of the rows, in one
 // launch; NDL_ERR_UNSUPPORTED (nothing launched) unless n % 128 == 0,
 // n <= 4096 and x / aux sit on 16-byte boundaries.
 int launch_fake_a8_prepare(int mode, const float *x, const float *aux, int rows, int n, int bits, int8_t *values,
                            float *scales, float *offsets, int stride, cudaStream_t stream);
+// HadamardMlp.Apply on `count` residual rows with explicit factors (d1, d2,
+// b2, d3, d4, w1a, w1b, w2a, w2b, w3a, w3b, cond_v, cond_u), block per row.
+int launch_hadamard_mlp_rows(const float *const w[13], const float *pre_norm, const int32_t *perm_a,
+                             const int32_t *perm_b, int dim, int rows, int cols, float scale, float *residual, int count,
+                             cudaStream_t stream);
 // Several matrices of the same width and bits over one Prepare, few launches.
 int launch_cq_matmul_jobs(const CqMatmulJob *jobs, int n_jobs, int cols, int bits, const int8_t *values,
                           const float *scales, const float *offsets, int stride, int tokens, cudaStream_t stream);

@@ -395,24 +395,6 @@ void rope_tables(float theta, int qk, int positions, std::vector<float> &cs, std
         }
 }
 
-// MathF.Exp in double as the device's exp_rn, for the host-side sigmoid of
-// the attention gate logits (the same steps, so the same bits).
-float host_exp_rn(float x) {
-    if (x != x) return x;
-    if (x > 89.0f) return INFINITY;
-    if (x < -104.0f) return 0.0f;
-    const double xd = (double)x;
-    const double k = rint(xd * 1.4426950408889634);
-    const double r = (xd - k * 6.93147180369123816490e-01) - k * 1.90821492927058770002e-10;
-    double p = 1.6059043836821614599e-10;
-    const double c[] = {2.0876756987868098979e-09, 2.5052108385441718775e-08, 2.7557319223985890653e-07,
-                        2.7557319223985890653e-06, 2.4801587301587301587e-05, 1.9841269841269841270e-04,
-                        1.3888888888888888889e-03, 8.3333333333333333333e-03, 4.1666666666666666667e-02,
-                        1.6666666666666666667e-01, 0.5, 1.0, 1.0};
-    for (double ci : c) p = fma(p, r, ci);
-    return (float)scalbn(p, (int)k);
-}
-
 int cq_matmul(const CqView &w, const N3State *s, int tokens, int row_start, int row_end, float *y, int ldy,
               cudaStream_t st) {
     return ndl_cq_matmul(w.indices, w.norms, w.book->bytes, w.book->byte_scale, w.rows, w.cols, w.bits, s->act_values,

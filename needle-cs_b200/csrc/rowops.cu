@@ -154,14 +154,19 @@ __global__ void __launch_bounds__(256) fake_a8_kernel(const float *__restrict__ 
     }
 }
 
-// CTA-per-row form of fake_a8_kernel for rows of n % 4 == 0, n <= 4096 floats
-// on 16-byte boundaries, with the same arithmetic element for element: the
-// row stays in registers (float4 i on thread i % 128), the squares go through
-// shared memory and thread 0 sums them in ascending order with its next four
-// float4 loads issued ahead of the current adds (the add chain is the
-// kernel's critical path); the peak is a max over the CTA.  With kPrep the
-// rows go on into CQ Prepare (n % 128 == 0): warp w holds group w + 4 i of
-// the row as four consecutive elements per lane, and the prepared values,
+// CTA-per-row row ops for rows of n % 4 == 0, n <= 4096 floats on 16-byte
+// boundaries, the arithmetic of the scalar code element for element:
+//  MODE 0 RmsUnit (x * inverse), 1 ZeroCenteredRms (((1 + aux) x) inverse),
+//  2 MultiplyBySigmoid (x sigmoid(aux row)), 3 PostNormAdd (dst += gate[row]
+//  ((1 + aux) x) inverse), 4 ZeroCenteredRms then SiLU, 5 the row as it is;
+//  kFake adds Quant.FakeA8 (RmsFakeA8, CenteredRmsFakeA8, GateFakeA8 for
+//  modes 0..2, FakeA8 for mode 5), as fake_a8_kernel does.
+// The row stays in registers (float4 i on thread i % 128), the squares go
+// through shared memory and thread 0 sums them in ascending order with its
+// next four float4 loads issued ahead of the current adds (the add chain is
+// the kernel's critical path); the peak is a max over the CTA.  With kPrep
+// the rows go on into CQ Prepare (n % 128 == 0): warp w holds group w + 4 i
+// of the row as four consecutive elements per lane, and the prepared values,
 // scales and offsets are written instead of dst.
 constexpr int kFakeThreads = 128;
 constexpr int kFakeMaxVec = 8;
@@ -172,20 +177,15 @@ __device__ __forceinline__ float fake_warp_max(float v) {
     return v;
 }
 
-struct CqPrepOut {
-    int8_t *values;
-    float *scales, *offsets;
-    int stride, bits;
-};
-
-template <int MODE, bool kPrep = false>
-__global__ void __launch_bounds__(kFakeThreads) fake_a8_row_kernel(const float *__restrict__ x,
-                                                                   const float *__restrict__ aux,
-                                                                   const float *__restrict__ gate, int n,
-                                                                   float *__restrict__ dst, CqPrepOut prep) {
+template <int MODE, bool kPrep, bool kFake>
+__global__ void __launch_bounds__(kFakeThreads) row_op_kernel(const float *__restrict__ x,
+                                                              const float *__restrict__ aux,
+                                                              const float *__restrict__ gate, int n,
+                                                              float *__restrict__ dst, CqPrepOut prep) {
+    constexpr bool kRms = MODE == 0 || MODE == 1 || MODE == 3 || MODE == 4;
     pdl_enter();
     __shared__ float red[kFakeThreads / 32];
-    __shared__ float4 squares[MODE == 2 ? 1 : kFakeThreads * kFakeMaxVec];
+    __shared__ float4 squares[kRms ? kFakeThreads * kFakeMaxVec : 1];
     const int row = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nv = n >> 2;
     const float4 *in = reinterpret_cast<const float4 *>(x + (size_t)row * n);
     const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -196,7 +196,7 @@ __global__ void __launch_bounds__(kFakeThreads) fake_a8_row_kernel(const float *
         v[i] = idx < nv ? in[idx] : zero;
     }
     float inverse = 0.0f;
-    if (MODE != 2) {
+    if (kRms) {
 #pragma unroll
         for (int i = 0; i < kFakeMaxVec; i++) {
             const int idx = tid + i * kFakeThreads;
@@ -260,34 +260,40 @@ __global__ void __launch_bounds__(kFakeThreads) fake_a8_row_kernel(const float *
         if (idx < nv) {
             float *e = reinterpret_cast<float *>(&v[i]);
             float4 a = zero;
-            if (MODE == 1) a = reinterpret_cast<const float4 *>(aux)[idx];
+            if (MODE == 1 || MODE == 4) a = reinterpret_cast<const float4 *>(aux)[idx];
             if (MODE == 2) a = reinterpret_cast<const float4 *>(aux + (size_t)row * n)[idx];
             const float *av = reinterpret_cast<const float *>(&a);
 #pragma unroll
             for (int k = 0; k < 4; k++) {
                 if (MODE == 0) e[k] = __fmul_rn(e[k], inverse);
-                else if (MODE == 1) e[k] = __fmul_rn(__fmul_rn(__fadd_rn(1.0f, av[k]), e[k]), inverse);
-                else e[k] = __fmul_rn(e[k], sigmoid_rn(av[k]));
+                else if (MODE == 1 || MODE == 4) e[k] = __fmul_rn(__fmul_rn(__fadd_rn(1.0f, av[k]), e[k]), inverse);
+                else if (MODE == 2) e[k] = __fmul_rn(e[k], sigmoid_rn(av[k]));
+                if (MODE == 4) e[k] = __fmul_rn(e[k], sigmoid_rn(e[k]));
                 peak = fmaxf(peak, fabsf(e[k]));
             }
         }
     }
-    peak = fake_warp_max(peak);
-    if (lane == 0) red[warp] = peak;
-    __syncthreads();
-    peak = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
-    const float scale = peak > 0.0f ? __fdiv_rn(peak, 127.0f) : 1.0f;
-    const float round = __fdiv_rn(1.0f, scale);
+    float scale = 1.0f, round = 1.0f;
+    if (kFake) {
+        peak = fake_warp_max(peak);
+        if (lane == 0) red[warp] = peak;
+        __syncthreads();
+        peak = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+        scale = peak > 0.0f ? __fdiv_rn(peak, 127.0f) : 1.0f;
+        round = __fdiv_rn(1.0f, scale);
+    }
 #pragma unroll
     for (int i = 0; i < kFakeMaxVec; i++) {
         const int idx = tid + i * kFakeThreads;
         if (idx < nv) {  // warp-uniform when kPrep (nv % 32 == 0)
             float *e = reinterpret_cast<float *>(&v[i]);
+            if (kFake) {
 #pragma unroll
-            for (int k = 0; k < 4; k++) {
-                // Scalar.RoundEven as in fake_a8_kernel
-                const float r = __fsub_rn(__fadd_rn(__fmul_rn(e[k], round), 12582912.0f), 12582912.0f);
-                e[k] = __fmul_rn(fminf(fmaxf(r, -128.0f), 127.0f), scale);
+                for (int k = 0; k < 4; k++) {
+                    // Scalar.RoundEven as in fake_a8_kernel
+                    const float r = __fsub_rn(__fadd_rn(__fmul_rn(e[k], round), 12582912.0f), 12582912.0f);
+                    e[k] = __fmul_rn(fminf(fmaxf(r, -128.0f), 127.0f), scale);
+                }
             }
             if (kPrep) {
                 float w[4] = {e[0], e[1], e[2], e[3]};
@@ -698,6 +704,29 @@ __global__ void __launch_bounds__(256) slot_hadamard_mlp_kernel(KtMlpArgs a) {
     });
 }
 
+int launch_hadamard_mlp_rows(const float *const w[13], const float *pre_norm, const int32_t *perm_a,
+                             const int32_t *perm_b, int dim, int rows, int cols, float scale, float *residual, int count,
+                             cudaStream_t stream) {
+    if (count == 0) return NDL_OK;
+    KtMlpArgs a{};
+    for (int k = 0; k < 13; k++) a.w[k] = w[k];
+    a.pre_norm = pre_norm;
+    a.perm_a = perm_a;
+    a.perm_b = perm_b;
+    a.dim = dim;
+    a.rows = rows;
+    a.cols = cols;
+    a.scale = scale;
+    a.residual = residual;
+    a.row_stride = dim;
+    const size_t smem = mlp_smem_floats(dim, rows, cols) * 4;
+    if (smem > 200 * 1024) return set_error(NDL_ERR_UNSUPPORTED, "hadamard_mlp: dim %d x width %d too large", dim,
+                                            rows * cols);
+    NDL_CUDA(cudaFuncSetAttribute(slot_hadamard_mlp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    launch_kernel(slot_hadamard_mlp_kernel, dim3((unsigned)count), dim3(256), smem, stream, a);
+    return check_launch("hadamard_mlp_rows");
+}
+
 int launch_slot_hadamard_mlp(const KtMlpArgs &a, cudaStream_t stream) {
     const size_t smem = mlp_smem_floats(a.dim, a.rows, a.cols) * 4;
     if (smem > 200 * 1024) return set_error(NDL_ERR_UNSUPPORTED, "hadamard_mlp: dim %d x width %d too large", a.dim,
@@ -743,15 +772,7 @@ int launch_fake_a8(int mode, const float *x, const float *aux, const float *gate
     if (rows == 0) return NDL_OK;
     if (n % 4 == 0 && n <= 4 * kFakeThreads * kFakeMaxVec && aligned(x, 16) && aligned(dst, 16) &&
         (mode == 0 || aligned(aux, 16))) {
-        const dim3 grid((unsigned)rows), block(kFakeThreads);
-        const CqPrepOut none{};
-        switch (mode) {
-            case 0: launch_kernel(fake_a8_row_kernel<0>, grid, block, 0, stream, x, aux, gate, n, dst, none); break;
-            case 1: launch_kernel(fake_a8_row_kernel<1>, grid, block, 0, stream, x, aux, gate, n, dst, none); break;
-            case 2: launch_kernel(fake_a8_row_kernel<2>, grid, block, 0, stream, x, aux, gate, n, dst, none); break;
-            default: launch_kernel(fake_a8_row_kernel<3>, grid, block, 0, stream, x, aux, gate, n, dst, none); break;
-        }
-        return check_launch("fake_a8_row");
+        return launch_row_op(mode, mode != 3, x, aux, gate, rows, n, dst, nullptr, stream);
     }
     const dim3 grid(blocks_for((long long)rows * 32, 256)), block(256);
     switch (mode) {
@@ -763,20 +784,51 @@ int launch_fake_a8(int mode, const float *x, const float *aux, const float *gate
     return check_launch("fake_a8");
 }
 
-int launch_fake_a8_prepare(int mode, const float *x, const float *aux, int rows, int n, int bits, int8_t *values,
-                           float *scales, float *offsets, int stride, cudaStream_t stream) {
-    if (mode < 0 || mode > 2 || n % 128 != 0 || n > 4 * kFakeThreads * kFakeMaxVec || !aligned(x, 16) ||
-        (mode != 0 && !aligned(aux, 16)) || stride < n / 128)
+template <int MODE, bool kPrep, bool kFake>
+static void row_op_launch(dim3 grid, const float *x, const float *aux, const float *gate, int n, float *dst,
+                          const CqPrepOut &prep, cudaStream_t stream) {
+    launch_kernel(row_op_kernel<MODE, kPrep, kFake>, grid, dim3(kFakeThreads), 0, stream, x, aux, gate, n, dst, prep);
+}
+
+template <int MODE>
+static void row_op_dispatch(bool fake, bool with_prep, dim3 grid, const float *x, const float *aux, const float *gate,
+                            int n, float *dst, const CqPrepOut &prep, cudaStream_t stream) {
+    if (with_prep) {
+        if (fake) row_op_launch<MODE, true, true>(grid, x, aux, gate, n, dst, prep, stream);
+        else row_op_launch<MODE, true, false>(grid, x, aux, gate, n, dst, prep, stream);
+    } else {
+        if (fake) row_op_launch<MODE, false, true>(grid, x, aux, gate, n, dst, prep, stream);
+        else row_op_launch<MODE, false, false>(grid, x, aux, gate, n, dst, prep, stream);
+    }
+}
+
+int launch_row_op(int mode, bool fake, const float *x, const float *aux, const float *gate, int rows, int n,
+                  float *dst, const CqPrepOut *prep, cudaStream_t stream) {
+    const bool uses_aux = mode == 1 || mode == 2 || mode == 3 || mode == 4;
+    if (mode < 0 || mode > 5 || (mode == 3 && (fake || prep)) || n % (prep ? 128 : 4) != 0 ||
+        n > 4 * kFakeThreads * kFakeMaxVec || !aligned(x, 16) || (uses_aux && !aligned(aux, 16)) ||
+        (!prep && !aligned(dst, 16)) || (prep && prep->stride < n / 128))
         return NDL_ERR_UNSUPPORTED;
     if (rows == 0) return NDL_OK;
-    const dim3 grid((unsigned)rows), block(kFakeThreads);
-    const CqPrepOut prep{values, scales, offsets, stride, bits};
+    const dim3 grid((unsigned)rows);
+    const CqPrepOut none{}, &p = prep ? *prep : none;
+    const bool wp = prep != nullptr;
     switch (mode) {
-        case 0: launch_kernel(fake_a8_row_kernel<0, true>, grid, block, 0, stream, x, aux, nullptr, n, nullptr, prep); break;
-        case 1: launch_kernel(fake_a8_row_kernel<1, true>, grid, block, 0, stream, x, aux, nullptr, n, nullptr, prep); break;
-        default: launch_kernel(fake_a8_row_kernel<2, true>, grid, block, 0, stream, x, aux, nullptr, n, nullptr, prep); break;
+        case 0: row_op_dispatch<0>(fake, wp, grid, x, aux, gate, n, dst, p, stream); break;
+        case 1: row_op_dispatch<1>(fake, wp, grid, x, aux, gate, n, dst, p, stream); break;
+        case 2: row_op_dispatch<2>(fake, wp, grid, x, aux, gate, n, dst, p, stream); break;
+        case 3: row_op_launch<3, false, false>(grid, x, aux, gate, n, dst, p, stream); break;
+        case 4: row_op_dispatch<4>(fake, wp, grid, x, aux, gate, n, dst, p, stream); break;
+        default: row_op_dispatch<5>(fake, wp, grid, x, aux, gate, n, dst, p, stream); break;
     }
-    return check_launch("fake_a8_prepare");
+    return check_launch("row_op");
+}
+
+int launch_fake_a8_prepare(int mode, const float *x, const float *aux, int rows, int n, int bits, int8_t *values,
+                           float *scales, float *offsets, int stride, cudaStream_t stream) {
+    if (mode < 0 || mode > 2) return NDL_ERR_UNSUPPORTED;
+    const CqPrepOut prep{values, scales, offsets, stride, bits};
+    return launch_row_op(mode, true, x, aux, nullptr, rows, n, nullptr, &prep, stream);
 }
 
 }  // namespace ndl

@@ -20,6 +20,17 @@ PU64 = _c.POINTER(_c.c_uint64)
 
 _SIGS = {
     "ndo_xorshift_next": (U64, [PU64]),
+    # the Whistle front end (whistle_oracle.c)
+    "ndo_log_rn": (F, [F]),
+    "ndo_log_rn_array": (None, [P, I, P]),
+    "ndo_frontend_tables": (None, [I, I, P, I, P, P, P, P, P, P]),
+    "ndo_mel_frame": (F, [P, I, I, P, P, P, P, P, I, P, P, P]),
+    "ndo_normalize_columns": (None, [P, I, I]),
+    "ndo_whistle_rope_tables": (None, [F, I, I, P, P]),
+    "ndo_cross_position_tables": (None, [I, I, P, P]),
+    "ndo_silu": (None, [P, I]),
+    "ndo_glu": (None, [P, P, P, I]),
+    "ndo_multiply_by_sigmoid": (None, [P, P, I]),
     "ndo_xorshift_int": (I, [PU64, I, I]),
     "ndo_xorshift_float": (F, [PU64, F]),
     "ndo_fill_uniform": (None, [P, I, PU64, F]),

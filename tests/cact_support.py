@@ -227,3 +227,110 @@ def needle3_decoder_archive(seed=0, **geometry):
     a.dense("final_norm", 0, d, values=small(d, 0.1))
     a.raw(b"needle tokenizer blob \x00\x01\x02")
     return a
+
+
+MLP_NAMES = ("d1", "d2", "b2", "d3", "d4", "w1a", "w1b", "w2a", "w2b", "w3a", "w3b", "cond_v", "cond_u")
+
+
+def mel_bank(fft, mels, rate):
+    """A triangular mel filterbank [fft/2 + 1][mels] (nonnegative, each bin
+    in at most two adjacent filters), fp32."""
+    def hz_to_mel(f):
+        return 2595.0 * np.log10(1.0 + f / 700.0)
+
+    bins = fft // 2 + 1
+    edges = 700.0 * (10 ** (np.linspace(hz_to_mel(0.0), hz_to_mel(rate / 2), mels + 2) / 2595.0) - 1.0)
+    freqs = np.linspace(0, rate / 2, bins)
+    bank = np.zeros((bins, mels), np.float32)
+    for m in range(mels):
+        lo, mid, hi = edges[m], edges[m + 1], edges[m + 2]
+        up = (freqs - lo) / (mid - lo)
+        down = (hi - freqs) / (hi - mid)
+        bank[:, m] = np.maximum(0.0, np.minimum(up, down)).astype(np.float32)
+    return bank
+
+
+def whistle_archive(seed=0, encoder_layers=2, conv_kernel=7, stem_width=128, mels=80, fft=512, window=400, hop=160,
+                    sample_rate=16000, **geometry):
+    """A Needle-3 archive with a Whistle audio section in AudioWeights' order
+    (src/Needle/Audio.cs:117-149): the 13-entry manifest; per decoder layer
+    the CrossWeights (norm, Q, K, V, gate, out, q/k norms, post norm, mix
+    logit); the position-mix logit; per encoder layer the EncoderLayer (six
+    norms, Q/K/V/gate/out, q/k norms, attention gate logit, the two pointwise
+    convs, the depthwise taps, two MlpWeights); the encoder's
+    HyperConnections (no permutations); the final norm; the three-stage stem
+    (first 3x3 conv, depthwise + pointwise twice, the output projection);
+    the mel filterbank.  Values are tame (norm scales near zero, small conv
+    taps and MLP factors) so activations stay finite through the encoder."""
+    a = needle3_decoder_archive(seed=seed, **geometry)
+    a.records.pop()  # the tokenizer goes last again below
+    g, rng = a.g, a.rng
+    d, L, E, s = g["dim"], g["layers"], encoder_layers, stem_width
+    H, KV, QK, VD = g["heads"], g["kv_heads"], g["qk_dim"], g["v_dim"]
+    qw, kw, vw, ow = H * QK, KV * QK, KV * VD, H * VD
+    g.update(encoder_layers=E, conv_kernel=conv_kernel, stem_width=s, mels=mels, fft=fft, window=window, hop=hop,
+             sample_rate=sample_rate)
+    k = [0]
+
+    def small(n, sd):
+        return rng.normal(0, sd, n).astype(np.float16).view(np.uint16)
+
+    def dense(n, sd=None, values=None, fp16=True):
+        if values is None:
+            values = small(n, sd) if fp16 else rng.normal(0, sd, n).astype(np.float32)
+        a.dense("audio", k[0], n, fp16=fp16, values=values)
+        k[0] += 1
+
+    def cq(rows, cols, bits=2):
+        a.cq("audio", k[0], rows, cols, bits)
+        k[0] += 1
+
+    manifest = np.zeros(13, np.float32)
+    manifest[3:13] = [E, 4, conv_kernel, s, 3, mels, sample_rate, fft, window, hop]
+    dense(13, values=manifest, fp16=False)
+    for _ in range(L):  # CrossWeights
+        dense(d, 0.1)
+        cq(H * QK, d)
+        cq(H * QK, d)
+        cq(H * VD, d)
+        cq(H * VD, d)
+        cq(d, H * VD)
+        dense(QK, 0.1)
+        dense(QK, 0.1)
+        dense(d, 0.1)
+        dense(1, 1.0, fp16=False)
+    dense(1, 1.0, fp16=False)  # position mix logit
+    for _ in range(E):  # EncoderLayer
+        for _ in range(6):
+            dense(d, 0.1)
+        cq(qw, d)
+        cq(kw, d)
+        cq(vw, d)
+        cq(ow, d)
+        cq(d, ow)
+        dense(QK, 0.1)
+        dense(QK, 0.1)
+        dense(1, 1.0, fp16=False)  # attention gate logit
+        cq(2 * d, d)
+        cq(d, d)
+        dense(conv_kernel * d, 0.3)
+        for _ in range(2):  # MlpWeights
+            for n in MLP_NAMES:
+                size = a._layer_size("layer.mlp." + n)
+                dense(size, 0.1 if n.startswith(("w", "cond")) else 0.3)
+    for n, count in (("a_pre", E), ("a_post", E), ("a_res", E), ("b_pre", 4 * E), ("b_post", 4 * E),
+                     ("b_res", 16 * E)):
+        dense(count, 0.5)
+    cq(4 * E, 4 * d, 4)
+    cq(4 * E, 4 * d, 4)
+    cq(16 * E, 4 * d, 4)
+    dense(d, 0.1)  # final norm
+    dense(9 * s, 0.3)  # stem first
+    dense(9 * s, 0.3)  # stem depthwise 1
+    cq(s, s)
+    dense(9 * s, 0.3)  # stem depthwise 2
+    cq(s, s)
+    cq(d, 10 * s)  # stem out
+    dense(None, values=mel_bank(fft, mels, sample_rate).reshape(-1), fp16=False)
+    a.raw(b"needle tokenizer blob \x00\x01\x02")
+    return a
