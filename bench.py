@@ -1158,6 +1158,120 @@ def needle3_cpu_sample(a, steps=2):
                       f"(oracle/needle3.py over oracle/needle_oracle.c), 1 thread; {host_cpu()[0]}"}
 
 
+WHISTLE_SHAPE = dict(dim=384, heads=6, kv_heads=6, qk_dim=48, v_dim=64, layers=4, vocab=8192, hada_n=512,
+                     engram_sub=128, engram_tables=3, sites=[1], global_mask=0b1111)
+WHISTLE_AUDIO = dict(encoder_layers=6, conv_kernel=15, stem_width=128, mels=80, fft=512, window=400, hop=160,
+                     sample_rate=16000)
+WHISTLE_SECONDS = 20.0
+
+
+def whistle_bench_archive(seed):
+    """A synthetic archive of the Whistle speech model's shape: the decoder of BASELINE's config 4 (4 layers,
+    d 384, 6 heads; head dims 48 / 64 as the loader requires) in the Needle-3 layout with its cross weights, and an audio section of 6 encoder
+    layers (conv kernel 15, stem width 128, 80 mels, fft 512 / window 400 / hop 160 at 16 kHz).  whistle.cact
+    is absent here; these counts stand in for its own."""
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    from cact_support import whistle_archive
+
+    return whistle_archive(seed=seed, **WHISTLE_AUDIO, **WHISTLE_SHAPE)
+
+
+def whistle_cpu_sample(a, seconds=5.0):
+    """The scalar-tier chain of the same encoder (oracle/whistle.py over oracle/whistle_oracle.c and
+    needle_oracle.c, 1 thread) on `seconds` of the same synthetic audio."""
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    from whistle_support import speech_like, whistle_oracle
+
+    o = whistle_oracle(a)
+    pcm = speech_like(seconds, seed=0)
+    t0 = time.perf_counter()
+    o.encode(pcm)
+    o.build_memory()
+    dt = time.perf_counter() - t0
+    return {"value": seconds / dt, "unit": "audio s/s", "cores": 1, "kind": "port",
+            "sample": f"{seconds:g} s of synthetic audio through Encode + BuildCrossMemory, the scalar-tier chain "
+                      f"(oracle/whistle.py), 1 thread; {host_cpu()[0]}"}
+
+
+def run_whistle(args, rank, world, local):
+    """Row f4: Whistle.Encode + BuildCrossMemory through ndl_whistle_* on a synthetic archive of the speech
+    model's shape, a 20 s clip per step (the reference's published Whistle figure is for a 20 s clip).
+    value = audio seconds encoded per second of device time (CUDA events on the encoder's stream around the
+    timed steps, PCM already on the device; max over ranks); e2e = the same through ndl_whistle_encode with
+    the PCM copied from pinned host memory and the encoder output read back every step."""
+    import torch
+
+    pkg = entry.load_package()
+    pkg.lib()
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    cact = __import__("needle_cs_b200.model", fromlist=["model"])
+    wmod = __import__("needle_cs_b200.whistle", fromlist=["whistle"])
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    from whistle_support import speech_like
+
+    a = whistle_bench_archive(seed=5)
+    m = cact.Model(a.build(), device=local)
+    w = wmod.Whistle(m, max_seconds=WHISTLE_SECONDS)
+    pcm_host = torch.from_numpy(speech_like(WHISTLE_SECONDS, seed=rank)).pin_memory()
+    pcm_dev = pcm_host.to(device)
+    n = pcm_host.numel()
+    from needle_cs_b200._native import call
+
+    for _ in range(args.warmup):
+        call("ndl_whistle_encode_device", w._h, pcm_dev.data_ptr(), n)
+    torch.cuda.synchronize()
+    stream = torch.cuda.ExternalStream(w.stream())
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    with ClockSampler(torch.cuda.get_device_properties(device).uuid) as clocks:
+        e0.record(stream)
+        for _ in range(args.steps):
+            call("ndl_whistle_encode_device", w._h, pcm_dev.data_ptr(), n)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1), world)
+    import ctypes
+
+    fr = ctypes.c_int()
+    call("ndl_whistle_frames", w._h, ctypes.byref(fr), None)
+    frames = fr.value
+    out = np.empty((frames, m.info["dim"]), np.float32)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        w.encode(pcm_host.numpy())
+        out = w.encoder_output()
+    wall = max_over_ranks((time.perf_counter() - t0) * 1e3, world)
+    value = world * WHISTLE_SECONDS * args.steps / (ms * 1e-3)
+    E, L, d = WHISTLE_AUDIO["encoder_layers"], WHISTLE_SHAPE["layers"], WHISTLE_SHAPE["dim"]
+    weights = sum(len(r[4]) for r in a.records if r[0] == "audio")
+    achieved = weights / (ms * 1e-3 / args.steps) / 1e9
+    peak, peak_source = hbm_peak()
+    line = {"metric": "whistle encode audio seconds/sec/box", "value": value, "unit": "audio s/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32 front end, u2/u4 codes x int8 -> int32, f32",
+            "data": "synthetic",
+            "config": {"workload": "whistle_encode", "model": "synthetic archive of the Whistle speech model's shape",
+                       "clip_seconds": WHISTLE_SECONDS, "frames": frames, "geometry": dict(WHISTLE_SHAPE),
+                       "audio": dict(WHISTLE_AUDIO), "weight_bytes": weights,
+                       "l2": "weights fit L2; each step reads them once per layer pass"},
+            "roofline": {"bound": "hbm", "kernel": "the whole encode (latency-bound chain of small kernels)",
+                         "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "traffic": None, "peak_source": peak_source, "algorithmic_bytes_per_step": weights},
+            "e2e": {"value": world * WHISTLE_SECONDS * args.steps / (wall * 1e-3), "unit": "audio s/s",
+                    "h2d_bytes_per_step": n * 4, "d2h_bytes_per_step": out.nbytes},
+            # per encode: front end 3, stem 11, lanes + fill 2, 23 a layer, final 2, cross rows and Prepare 2,
+            # 2 per decoder layer
+            "gpu_launches": args.steps * (3 + 11 + 2 + 23 * E + 2 + 2 + 2 * L), "clocks": clocks.summary()}
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        entry.load_oracle()
+        line["cpu_baseline"] = whistle_cpu_sample(a)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    w.close()
+    m.close()
+
+
 def case_attention(steps=4, rows=512, seed=5):
     entry.load_package()
     from needle_cs_b200.engine import BatchedEngine, SyntheticDecoder
@@ -1200,7 +1314,7 @@ def case_gemm(m, n, k, calls=5):
 
 
 WORKLOADS = {"cfg1": GemvWorkload, "cfg2": DecodeWorkload, "cfg3": ServingWorkload, "cfg4": BeamWorkload,
-             "cfg5": DecodeWorkload, "prefix": None, "cq": CqWorkload, "needle3": None}
+             "cfg5": DecodeWorkload, "prefix": None, "cq": CqWorkload, "needle3": None, "whistle": None}
 DECODE = ("cfg2", "cfg5")
 
 
@@ -1226,6 +1340,16 @@ def run_reference(args, rank, world):
                           "dtype": "u2/u4 codes x int8 -> int32, f32", "data": "synthetic",
                           "config": {"workload": "needle3_decode"}, "cpu_baseline": base,
                           "e2e": {"value": base["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                                  "d2h_bytes_per_step": 0}}), flush=True)
+        return
+    if args.workload == "whistle":
+        base = whistle_cpu_sample(whistle_bench_archive(seed=5))
+        print(json.dumps({"impl": "reference", "metric": "whistle encode audio seconds/sec/box", "value": base["value"],
+                          "unit": "audio s/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+                          "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                          "dtype": "f32 front end, u2/u4 codes x int8 -> int32, f32", "data": "synthetic",
+                          "config": {"workload": "whistle_encode"}, "cpu_baseline": base,
+                          "e2e": {"value": base["value"], "unit": "audio s/s", "h2d_bytes_per_step": 0,
                                   "d2h_bytes_per_step": 0}}), flush=True)
         return
     wl = make_workload(args.workload, args)
@@ -1504,6 +1628,8 @@ def main():
             run_prefix(args, rank, world, local)
         elif args.workload == "needle3":
             run_needle3(args, rank, world, local)
+        elif args.workload == "whistle":
+            run_whistle(args, rank, world, local)
         else:
             run_ours(args, rank, world, local)
     finally:

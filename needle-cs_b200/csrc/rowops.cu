@@ -635,16 +635,20 @@ __global__ void __launch_bounds__(256) slot_hadamard_mlp_kernel(KtMlpArgs a) {
 #pragma unroll 16
         for (int i = 0; i < dim; i++) sum = __fadd_rn(sum, scratch[i]);
         weights[0] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, (float)dim), 1e-6f)));
-    } else if (tid >= 32) {  // meanwhile the other warps stage the Kronecker factors
+    } else if (tid >= 32) {  // meanwhile the other warps stage the Kronecker factors, all six in one pass
         const int sizes[6] = {input_rows * rows, cols * cols, rows * rows, cols * cols, rows * rows, cols * cols};
-        float *dsts[6] = {left1, right1, left2, right2, left3, right3};
-#pragma unroll
-        for (int f = 0; f < 6; f++) {
-            const float *__restrict__ src = a.w[5 + f];
-            float *dst = dsts[f];
-            mlp_batched<8>(sizes[f], tid - 32, nt - 32, [&](int i) { return __ldg(src + i); },
-                           [&](int i, float v) { dst[i] = v; });
-        }
+        int ends[6];
+        ends[0] = sizes[0];
+        for (int f = 1; f < 6; f++) ends[f] = ends[f - 1] + sizes[f];
+        // left1 .. right3 are contiguous in shared memory in this order
+        mlp_batched<16>(
+            ends[5], tid - 32, nt - 32,
+            [&](int i) {
+                int f = 0;
+                while (f < 5 && i >= ends[f]) f++;
+                return __ldg(a.w[5 + f] + (i - (f ? ends[f - 1] : 0)));
+            },
+            [&](int i, float v) { left1[i] = v; });
     }
     __syncthreads();
     const float inv = weights[0];

@@ -83,14 +83,18 @@ __device__ __forceinline__ float log_rn(float x) {
 }
 
 // FeatureJob.Execute for one frame per CTA (Frontend.cs:100-130) with the
-// scalar Butterflies (:205-225).  peak_bits gets the max over frames as the
-// bits of a nonnegative float (an integer max orders them the same way).
+// scalar Butterflies (:205-225).  Mel m sums the bins in [mel_lo[m],
+// mel_hi[m]) whose range holds it (outside them no bin's range does), in
+// ascending order.  peak_bits gets the max over frames as the bits of a
+// nonnegative float (an integer max orders them the same way).
 __global__ void __launch_bounds__(256) wh_mel_kernel(const float *__restrict__ padded, int hop, int fft, int window,
                                                      const float *__restrict__ hann, const float *__restrict__ cosines,
                                                      const float *__restrict__ sines, const int32_t *__restrict__ bitrev,
                                                      const float *__restrict__ bank, int mels,
                                                      const int32_t *__restrict__ mel_first,
-                                                     const int32_t *__restrict__ mel_count, float *__restrict__ mel,
+                                                     const int32_t *__restrict__ mel_count,
+                                                     const int32_t *__restrict__ mel_lo,
+                                                     const int32_t *__restrict__ mel_hi, float *__restrict__ mel,
                                                      unsigned *__restrict__ peak_bits) {
     pdl_enter();
     extern __shared__ float wh_fft[];
@@ -122,7 +126,7 @@ __global__ void __launch_bounds__(256) wh_mel_kernel(const float *__restrict__ p
     __syncthreads();
     for (int m = threadIdx.x; m < mels; m += blockDim.x) {
         float acc = 0.0f;
-        for (int k = 0; k <= fft / 2; k++) {
+        for (int k = mel_lo[m]; k < mel_hi[m]; k++) {  // the bins whose range can hold m, ascending
             const int first = mel_first[k];
             if (m >= first && m < first + mel_count[k])
                 acc = __fadd_rn(acc, __fmul_rn(power[k], bank[(size_t)k * mels + m]));
@@ -142,24 +146,55 @@ __global__ void wh_log_kernel(float *__restrict__ mel, long long n, const unsign
     mel[i] = log_rn(__fadd_rn(mel[i], floor));
 }
 
-// Whistle.Normalize's scalar branch (Whistle.cs:263-272), thread per column.
-__global__ void wh_normalize_kernel(float *__restrict__ x, int rows, int cols) {
+// Whistle.Normalize's scalar branch (Whistle.cs:263-272), thread per
+// column: in double, the sum of the column in row order / rows, then the
+// squares of x - mean in row order, sd = sqrt(squares / max(rows - 1, 1));
+// den = sd + 1e-5.  Each thread loads 16 rows ahead of its adds (the add
+// chain is the kernel's critical path).
+__global__ void wh_moments_kernel(const float *__restrict__ x, int rows, int cols, double *__restrict__ mean_out,
+                                  double *__restrict__ den_out) {
     pdl_enter();
     const int c = blockIdx.x * blockDim.x + threadIdx.x;
     if (c >= cols) return;
     const int denom = rows - 1 > 1 ? rows - 1 : 1;
     double sum = 0.0;
-    for (int r = 0; r < rows; r++) sum = __dadd_rn(sum, (double)x[(size_t)r * cols + c]);
+    int r = 0;
+    for (; r + 16 <= rows; r += 16) {
+        float v[16];
+#pragma unroll
+        for (int k = 0; k < 16; k++) v[k] = x[(size_t)(r + k) * cols + c];
+#pragma unroll
+        for (int k = 0; k < 16; k++) sum = __dadd_rn(sum, (double)v[k]);
+    }
+    for (; r < rows; r++) sum = __dadd_rn(sum, (double)x[(size_t)r * cols + c]);
     const double mean = __ddiv_rn(sum, (double)rows);
     double squares = 0.0;
-    for (int r = 0; r < rows; r++) {
+    for (r = 0; r + 16 <= rows; r += 16) {
+        float v[16];
+#pragma unroll
+        for (int k = 0; k < 16; k++) v[k] = x[(size_t)(r + k) * cols + c];
+#pragma unroll
+        for (int k = 0; k < 16; k++) {
+            const double dv = __dsub_rn((double)v[k], mean);
+            squares = __dadd_rn(squares, __dmul_rn(dv, dv));
+        }
+    }
+    for (; r < rows; r++) {
         const double dv = __dsub_rn((double)x[(size_t)r * cols + c], mean);
         squares = __dadd_rn(squares, __dmul_rn(dv, dv));
     }
-    const double sd = __dsqrt_rn(__ddiv_rn(squares, (double)denom));
-    const double den = __dadd_rn(sd, 1e-5);
-    for (int r = 0; r < rows; r++)
-        x[(size_t)r * cols + c] = __double2float_rn(__ddiv_rn(__dsub_rn((double)x[(size_t)r * cols + c], mean), den));
+    mean_out[c] = mean;
+    den_out[c] = __dadd_rn(__dsqrt_rn(__ddiv_rn(squares, (double)denom)), 1e-5);
+}
+
+// x = (float)((x - mean) / den) per element.
+__global__ void wh_standardize_kernel(float *__restrict__ x, long long n, int cols, const double *__restrict__ mean,
+                                      const double *__restrict__ den) {
+    pdl_enter();
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const int c = (int)(i % cols);
+    x[i] = __double2float_rn(__ddiv_rn(__dsub_rn((double)x[i], mean[c]), den[c]));
 }
 
 // Stem stage 1 (ExecuteStageFirst, Whistle.cs:346-375): out[p][f][c] = SiLU
@@ -365,14 +400,21 @@ __global__ void __launch_bounds__(32 * kWhWarps) wh_attention_kernel(
     if (item >= frames * heads) return;
     float *sc = wh_scores + (size_t)warp * frames;
     const int t = item / heads, h = item - t * heads;
-    const int group = heads / kv, kh = h / group;
-    const int8_t *q = q8 + (size_t)t * heads * qk + h * qk;
+    const int group = heads / kv, kh = h / group, words = qk / 4;
+    // the query as int32 words (qk % 4 == 0, rows on 4-byte boundaries): the
+    // int dot by dp4a, the same exact int32 as the byte loop
+    int qw[kWhMaxHead / 4];
+    const int *qrow = reinterpret_cast<const int *>(q8 + (size_t)t * heads * qk + h * qk);
+#pragma unroll
+    for (int i = 0; i < kWhMaxHead / 4; i++) qw[i] = i < words ? qrow[i] : 0;
     const float scale = __fmul_rn(qs[(size_t)t * heads + h], inv_sqrt);
     float peak = -INFINITY;
     for (int j = lane; j < frames; j += 32) {
-        const int8_t *kr = keys + (size_t)j * kv * qk + kh * qk;
+        const int *kr = reinterpret_cast<const int *>(keys + (size_t)j * kv * qk + kh * qk);
         int dot = 0;
-        for (int d = 0; d < qk; d++) dot += (int)q[d] * (int)kr[d];
+#pragma unroll
+        for (int i = 0; i < kWhMaxHead / 4; i++)
+            if (i < words) dot = __dp4a(kr[i], qw[i], dot);
         const float s = __fmul_rn(__fmul_rn(__int2float_rn(dot), ks[(size_t)j * kv + kh]), scale);
         sc[j] = s;
         peak = fmaxf(peak, s);
@@ -384,14 +426,25 @@ __global__ void __launch_bounds__(32 * kWhWarps) wh_attention_kernel(
     if (lane == 0)
         for (int j = 0; j < frames; j++) total = __fadd_rn(total, sc[j]);
     total = __shfl_sync(0xffffffffu, total, 0);
-    for (int j = lane; j < frames; j += 32) sc[j] = __fdiv_rn(sc[j], total);
+    // p_j = e_j / total, then the PV weight p_j * vs_j, both per position
+    for (int j = lane; j < frames; j += 32) sc[j] = __fmul_rn(__fdiv_rn(sc[j], total), vs[(size_t)j * kv + kh]);
     __syncwarp();
+    const int8_t *vbase = values + kh * vd;
+    const size_t vstride = (size_t)kv * vd;
     for (int d = lane; d < vd; d += 32) {
         float acc = 0.0f;
-        for (int j = 0; j < frames; j++) {
-            const float w = __fmul_rn(sc[j], vs[(size_t)j * kv + kh]);
-            acc = __fadd_rn(acc, __fmul_rn(w, (float)values[(size_t)j * kv * vd + kh * vd + d]));
+        int j = 0;
+        for (; j + 4 <= frames; j += 4) {
+            float v[4], wj[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                v[u] = (float)vbase[(size_t)(j + u) * vstride + d];
+                wj[u] = sc[j + u];
+            }
+#pragma unroll
+            for (int u = 0; u < 4; u++) acc = __fadd_rn(acc, __fmul_rn(wj[u], v[u]));
         }
+        for (; j < frames; j++) acc = __fadd_rn(acc, __fmul_rn(sc[j], (float)vbase[(size_t)j * vstride + d]));
         out[(size_t)t * heads * vd + h * vd + d] = acc;
     }
 }
@@ -527,7 +580,8 @@ struct ndl_whistle {
     // device tables and buffers
     std::vector<void *> allocations;
     float *hann, *cosines, *sines, *rope_cos, *rope_sin, *pos_sin, *pos_cos;
-    int32_t *bitrev, *mel_first, *mel_count;
+    int32_t *bitrev, *mel_first, *mel_count, *mel_lo, *mel_hi;
+    double *col_mean, *col_den;
     unsigned *peak;
     float *padded, *mel, *stage0, *dw, *pw, *flat, *stem_out, *stream_a, *stream_b, *u, *residual, *pre, *post, *res,
         *hpre, *post_gate, *mix_logits, *mix, *quarters, *q, *k, *v, *gate, *qs, *ks, *vs, *attn_out, *proj, *glu,
@@ -733,6 +787,17 @@ int whistle_tables(ndl_whistle *w) {
         first[k] = f;
         count[k] = last >= f ? last - f + 1 : 0;
     }
+    std::vector<int32_t> lo(mels, 0), hi(mels, 0);  // per mel, the bins [lo, hi) whose ranges can hold it
+    for (int m = 0; m < mels; m++) {
+        int a = -1, b = -1;
+        for (int k = 0; k <= fft / 2; k++)
+            if (m >= first[k] && m < first[k] + count[k]) {
+                if (a < 0) a = k;
+                b = k;
+            }
+        lo[m] = a < 0 ? 0 : a;
+        hi[m] = a < 0 ? 0 : b + 1;
+    }
     std::vector<float> rc((size_t)F * (QK / 2)), rs((size_t)F * (QK / 2)), ps((size_t)F * half), pc((size_t)F * half);
     for (int p = 0; p < F; p++)
         for (int i = 0; i < QK / 2; i++) {
@@ -755,6 +820,10 @@ int whistle_tables(ndl_whistle *w) {
     WH_TRY(whistle_buf(w, &w->bitrev, bitrev.size()));
     WH_TRY(whistle_buf(w, &w->mel_first, first.size()));
     WH_TRY(whistle_buf(w, &w->mel_count, count.size()));
+    WH_TRY(whistle_buf(w, &w->mel_lo, lo.size()));
+    WH_TRY(whistle_buf(w, &w->mel_hi, hi.size()));
+    WH_TRY(whistle_buf(w, &w->col_mean, (size_t)mels));
+    WH_TRY(whistle_buf(w, &w->col_den, (size_t)mels));
     WH_TRY(whistle_buf(w, &w->rope_cos, rc.size()));
     WH_TRY(whistle_buf(w, &w->rope_sin, rs.size()));
     WH_TRY(whistle_buf(w, &w->pos_sin, ps.size()));
@@ -765,6 +834,8 @@ int whistle_tables(ndl_whistle *w) {
     NDL_CUDA(cudaMemcpy(w->bitrev, bitrev.data(), bitrev.size() * 4, cudaMemcpyHostToDevice));
     NDL_CUDA(cudaMemcpy(w->mel_first, first.data(), first.size() * 4, cudaMemcpyHostToDevice));
     NDL_CUDA(cudaMemcpy(w->mel_count, count.data(), count.size() * 4, cudaMemcpyHostToDevice));
+    NDL_CUDA(cudaMemcpy(w->mel_lo, lo.data(), lo.size() * 4, cudaMemcpyHostToDevice));
+    NDL_CUDA(cudaMemcpy(w->mel_hi, hi.data(), hi.size() * 4, cudaMemcpyHostToDevice));
     NDL_CUDA(cudaMemcpy(w->rope_cos, rc.data(), rc.size() * 4, cudaMemcpyHostToDevice));
     NDL_CUDA(cudaMemcpy(w->rope_sin, rs.data(), rs.size() * 4, cudaMemcpyHostToDevice));
     NDL_CUDA(cudaMemcpy(w->pos_sin, ps.data(), ps.size() * 4, cudaMemcpyHostToDevice));
@@ -872,13 +943,17 @@ int whistle_run(ndl_whistle *w, int samples) {
     NDL_CUDA(cudaMemsetAsync(w->peak, 0, sizeof(unsigned), st));
     launch_kernel(wh_mel_kernel, dim3((unsigned)l0), dim3(256), (size_t)(2 * fft + fft / 2 + 1) * 4, st, w->padded,
                   hop, fft, window, w->hann, w->cosines, w->sines, w->bitrev, w->bank, mels, w->mel_first,
-                  w->mel_count, w->mel, w->peak);
+                  w->mel_count, w->mel_lo, w->mel_hi, w->mel, w->peak);
     WH_LAUNCH("wh_mel");
     const long long nmel = (long long)l0 * mels;
     launch_kernel(wh_log_kernel, dim3(wh_blocks(nmel, 256)), dim3(256), 0, st, w->mel, nmel, (const unsigned *)w->peak);
     WH_LAUNCH("wh_log");
-    launch_kernel(wh_normalize_kernel, dim3(wh_blocks(mels, 128)), dim3(128), 0, st, w->mel, l0, mels);
-    WH_LAUNCH("wh_normalize");
+    launch_kernel(wh_moments_kernel, dim3(wh_blocks(mels, 32)), dim3(32), 0, st, (const float *)w->mel, l0, mels,
+                  w->col_mean, w->col_den);
+    WH_LAUNCH("wh_moments");
+    launch_kernel(wh_standardize_kernel, dim3(wh_blocks(nmel, 256)), dim3(256), 0, st, w->mel, nmel, mels,
+                  (const double *)w->col_mean, (const double *)w->col_den);
+    WH_LAUNCH("wh_standardize");
     // stem
     const long long n0 = (long long)l1 * 40 * s;
     launch_kernel(wh_stem1_kernel, dim3(wh_blocks(n0, 256)), dim3(256), 0, st, (const float *)w->mel, l0, mels,
@@ -1029,7 +1104,7 @@ extern "C" NDL_API int ndl_whistle_create(const ndl_model *m, int max_samples, n
                        E, conv, w->mels, w->fft, w->window, w->hop);
     else if (s < 128 || s % 128 != 0 || 10 * s > 8192 || d % 128 != 0 || 4 * d > 4096 ||
              (info.heads * info.v_dim) % 128 != 0 || info.qk_dim > kWhMaxHead || info.v_dim > kWhMaxHead ||
-             info.qk_dim % 2 != 0 || info.kv_heads < 1 || info.heads % info.kv_heads != 0 || info.hada_n <= 0)
+             info.qk_dim % 4 != 0 || info.kv_heads < 1 || info.heads % info.kv_heads != 0 || info.hada_n <= 0)
         rc = set_error(NDL_ERR_UNSUPPORTED,
                        "Whistle geometry: stem width %d, dim %d, heads %d x %d / %d, kv heads %d (the device encoder "
                        "takes CQ widths in 128-column groups, dim <= 1024, head dims <= %d)",
