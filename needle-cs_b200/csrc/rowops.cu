@@ -635,20 +635,30 @@ __global__ void __launch_bounds__(256) slot_hadamard_mlp_kernel(KtMlpArgs a) {
 #pragma unroll 16
         for (int i = 0; i < dim; i++) sum = __fadd_rn(sum, scratch[i]);
         weights[0] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, (float)dim), 1e-6f)));
-    } else if (tid >= 32) {  // meanwhile the other warps stage the Kronecker factors, all six in one pass
+    } else if (tid >= 32) {  // meanwhile the other warps stage the Kronecker factors
         const int sizes[6] = {input_rows * rows, cols * cols, rows * rows, cols * cols, rows * rows, cols * cols};
-        int ends[6];
-        ends[0] = sizes[0];
-        for (int f = 1; f < 6; f++) ends[f] = ends[f - 1] + sizes[f];
-        // left1 .. right3 are contiguous in shared memory in this order
-        mlp_batched<16>(
-            ends[5], tid - 32, nt - 32,
-            [&](int i) {
-                int f = 0;
-                while (f < 5 && i >= ends[f]) f++;
-                return __ldg(a.w[5 + f] + (i - (f ? ends[f - 1] : 0)));
-            },
-            [&](int i, float v) { left1[i] = v; });
+        float *dsts[6] = {left1, right1, left2, right2, left3, right3};
+        const int t2 = tid - 32, n2 = nt - 32;
+        int most = 0;
+        for (int f = 0; f < 6; f++) most = max(most, sizes[f]);
+        // every factor's loads of a chunk go out before any of its stores
+        for (int base = t2; base < most; base += 4 * n2) {
+            float v[6][4];
+#pragma unroll
+            for (int f = 0; f < 6; f++)
+#pragma unroll
+                for (int k = 0; k < 4; k++) {
+                    const int i = base + k * n2;
+                    v[f][k] = i < sizes[f] ? __ldg(a.w[5 + f] + i) : 0.0f;
+                }
+#pragma unroll
+            for (int f = 0; f < 6; f++)
+#pragma unroll
+                for (int k = 0; k < 4; k++) {
+                    const int i = base + k * n2;
+                    if (i < sizes[f]) dsts[f][i] = v[f][k];
+                }
+        }
     }
     __syncthreads();
     const float inv = weights[0];
