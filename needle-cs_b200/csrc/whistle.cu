@@ -36,6 +36,7 @@
 #include "common.cuh"
 #include "cq.cuh"
 #include "kernels.cuh"
+#include "kv.cuh"
 
 namespace ndl {
 namespace {
@@ -146,45 +147,88 @@ __global__ void wh_log_kernel(float *__restrict__ mel, long long n, const unsign
     mel[i] = log_rn(__fadd_rn(mel[i], floor));
 }
 
-// Whistle.Normalize's scalar branch (Whistle.cs:263-272), thread per
-// column: in double, the sum of the column in row order / rows, then the
-// squares of x - mean in row order, sd = sqrt(squares / max(rows - 1, 1));
-// den = sd + 1e-5.  Each thread loads 16 rows ahead of its adds (the add
-// chain is the kernel's critical path).
-__global__ void wh_moments_kernel(const float *__restrict__ x, int rows, int cols, double *__restrict__ mean_out,
-                                  double *__restrict__ den_out) {
+// Whistle.Normalize's scalar branch (Whistle.cs:263-272): per column, in
+// double, the sum in row order / rows, then the squares of x - mean in row
+// order, sd = sqrt(squares / max(rows - 1, 1)); den = sd + 1e-5.  One CTA,
+// a thread per column running its add chain over tiles of kMomRows rows in
+// shared memory; thread 0 brings the next tile (one contiguous block of the
+// [rows][cols] features) with a bulk copy while the chains run on the
+// current one, so the chains never wait on global memory.  A wait that runs
+// out sets *status (the encode then reports NDL_ERR_TIMEOUT).
+constexpr int kMomRows = 128;
+constexpr uint32_t kMomWaitLimit = 1u << 16;  // tests of about 1 us each
+
+__global__ void __launch_bounds__(128) wh_moments_kernel(const float *__restrict__ x, int rows, int cols,
+                                                         double *__restrict__ mean_out, double *__restrict__ den_out,
+                                                         int *__restrict__ status) {
     pdl_enter();
-    const int c = blockIdx.x * blockDim.x + threadIdx.x;
-    if (c >= cols) return;
-    const int denom = rows - 1 > 1 ? rows - 1 : 1;
-    double sum = 0.0;
-    int r = 0;
-    for (; r + 16 <= rows; r += 16) {
-        float v[16];
-#pragma unroll
-        for (int k = 0; k < 16; k++) v[k] = x[(size_t)(r + k) * cols + c];
-#pragma unroll
-        for (int k = 0; k < 16; k++) sum = __dadd_rn(sum, (double)v[k]);
+    extern __shared__ __align__(16) float mom_tile[];  // [2][kMomRows][cols]
+    __shared__ __align__(8) uint64_t bars[2];
+    __shared__ int failed;
+    const int tid = threadIdx.x;
+    const int tiles = (rows + kMomRows - 1) / kMomRows, denom = rows - 1 > 1 ? rows - 1 : 1;
+    if (tid == 0) {
+        mbar_init(&bars[0], 1);
+        mbar_init(&bars[1], 1);
+        fence_mbar_init();
+        failed = 0;
     }
-    for (; r < rows; r++) sum = __dadd_rn(sum, (double)x[(size_t)r * cols + c]);
-    const double mean = __ddiv_rn(sum, (double)rows);
-    double squares = 0.0;
-    for (r = 0; r + 16 <= rows; r += 16) {
-        float v[16];
+    __syncthreads();
+    auto issue = [&](int g) {  // sweep-wide tile g into buffer g & 1 (thread 0)
+        const int t = g % tiles, r0 = t * kMomRows, n = min(kMomRows, rows - r0);
+        const uint32_t bytes = (uint32_t)(((size_t)n * cols * 4 + 15) & ~(size_t)15);
+        fence_proxy_async_smem();
+        mbar_arrive_expect_tx(&bars[g & 1], bytes);
+        bulk_g2s(mom_tile + (size_t)(g & 1) * kMomRows * cols, x + (size_t)r0 * cols, bytes, &bars[g & 1]);
+    };
+    if (tid == 0) issue(0);
+    double mean = 0.0;
+    for (int pass = 0; pass < 2; pass++) {
+        double acc = 0.0;
+        for (int t = 0; t < tiles; t++) {
+            const int g = pass * tiles + t;
+            if (tid == 0 && g + 1 < 2 * tiles) issue(g + 1);  // its buffer was released by the barrier below
+            if (!mbar_wait_bounded(&bars[g & 1], (uint32_t)(g >> 1) & 1u, kMomWaitLimit)) failed = 1;
+            const float *cur = mom_tile + (size_t)(g & 1) * kMomRows * cols;
+            if (tid < cols && !failed) {
+                const int n = min(kMomRows, rows - t * kMomRows);
+                int r = 0;
+                for (; r + 16 <= n; r += 16) {  // 16 loads and conversions ahead of 16 chained adds
+                    double v[16];
 #pragma unroll
-        for (int k = 0; k < 16; k++) v[k] = x[(size_t)(r + k) * cols + c];
+                    for (int k = 0; k < 16; k++) v[k] = (double)cur[(r + k) * cols + tid];
 #pragma unroll
-        for (int k = 0; k < 16; k++) {
-            const double dv = __dsub_rn((double)v[k], mean);
-            squares = __dadd_rn(squares, __dmul_rn(dv, dv));
+                    for (int k = 0; k < 16; k++) {
+                        if (pass == 0) {
+                            acc = __dadd_rn(acc, v[k]);
+                        } else {
+                            const double dv = __dsub_rn(v[k], mean);
+                            acc = __dadd_rn(acc, __dmul_rn(dv, dv));
+                        }
+                    }
+                }
+                for (; r < n; r++) {
+                    const double v = (double)cur[r * cols + tid];
+                    if (pass == 0) {
+                        acc = __dadd_rn(acc, v);
+                    } else {
+                        const double dv = __dsub_rn(v, mean);
+                        acc = __dadd_rn(acc, __dmul_rn(dv, dv));
+                    }
+                }
+            }
+            __syncthreads();
+        }
+        if (tid < cols) {
+            if (pass == 0) {
+                mean = __ddiv_rn(acc, (double)rows);
+            } else {
+                mean_out[tid] = mean;
+                den_out[tid] = __dadd_rn(__dsqrt_rn(__ddiv_rn(acc, (double)denom)), 1e-5);
+            }
         }
     }
-    for (; r < rows; r++) {
-        const double dv = __dsub_rn((double)x[(size_t)r * cols + c], mean);
-        squares = __dadd_rn(squares, __dmul_rn(dv, dv));
-    }
-    mean_out[c] = mean;
-    den_out[c] = __dadd_rn(__dsqrt_rn(__ddiv_rn(squares, (double)denom)), 1e-5);
+    if (tid == 0 && failed) atomicOr(status, kStatusTimeout);
 }
 
 // x = (float)((x - mean) / den) per element.
@@ -384,38 +428,71 @@ __global__ void __launch_bounds__(32 * kWhWarps) wh_qkv_kernel(
 }
 
 // Scalar.AttentionHead (src/Needle/Scalar.cs:290-312) over every frame
-// (AttentionBatch.Span with Frames set: [0, frames), Blocks.cs:970-975), warp
-// per (frame, q head), kv head = head / (heads / kv): s_j = (dot_j * ks_j) *
-// (qs / sqrt(qk)); e_j = MathF.Exp(s_j - max) summed in frame order; p_j =
-// e_j / total; out[d] += (p_j * vs_j) * v_j[d] in frame order, two dims per
-// lane.  Scores live in the warp's shared slice [frames].
+// (AttentionBatch.Span with Frames set: [0, frames), Blocks.cs:970-975).  CTA
+// per (kv head, four (frame, grouped head) items): the kv head's int8 keys,
+// values and scales of every frame are staged in shared memory once, then
+// warp per item: s_j = (dot_j * ks_j) * (qs / sqrt(qk)) with dp4a dots;
+// e_j = MathF.Exp(s_j - max) summed in frame order; w_j = (e_j / total) * vs_j;
+// out[d] += w_j * v_j[d] in frame order, dims d and d + 32 of a lane side by
+// side.
 __global__ void __launch_bounds__(32 * kWhWarps) wh_attention_kernel(
     const int8_t *__restrict__ q8, const float *__restrict__ qs, int frames, int heads, int kv, int qk, int vd,
     float inv_sqrt, const int8_t *__restrict__ keys, const float *__restrict__ ks, const int8_t *__restrict__ values,
     const float *__restrict__ vs, float *__restrict__ out) {
     pdl_enter();
-    extern __shared__ float wh_scores[];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    extern __shared__ __align__(16) int wh_att[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, kh = blockIdx.y;
+    const int group = heads / kv, kwords = qk / 4, vwords = vd / 4;
+    int *kst = wh_att;                                               // [frames][qk / 4]
+    int *vst = kst + (size_t)frames * kwords;                        // [frames][vd / 4]
+    float *kss = reinterpret_cast<float *>(vst + (size_t)frames * vwords);  // [frames]
+    float *vss = kss + frames;                                        // [frames]
+    float *scores = vss + frames;                                     // [kWhWarps][frames]
+    {  // stage the kv head: 4-byte words, 16 loads in flight per thread
+        const int nk = frames * kwords, nv = frames * vwords, total = nk + nv + 2 * frames;
+        for (int base = threadIdx.x; base < total; base += 16 * blockDim.x) {
+            int v[16];
+#pragma unroll
+            for (int k = 0; k < 16; k++) {
+                const int i = base + k * blockDim.x;
+                if (i < nk) {
+                    const int j = i / kwords, wd = i - j * kwords;
+                    v[k] = reinterpret_cast<const int *>(keys + (size_t)j * kv * qk + kh * qk)[wd];
+                } else if (i < nk + nv) {
+                    const int j = (i - nk) / vwords, wd = i - nk - j * vwords;
+                    v[k] = reinterpret_cast<const int *>(values + (size_t)j * kv * vd + kh * vd)[wd];
+                } else if (i < nk + nv + frames) {
+                    v[k] = __float_as_int(ks[(size_t)(i - nk - nv) * kv + kh]);
+                } else if (i < total) {
+                    v[k] = __float_as_int(vs[(size_t)(i - nk - nv - frames) * kv + kh]);
+                }
+            }
+#pragma unroll
+            for (int k = 0; k < 16; k++) {
+                const int i = base + k * blockDim.x;
+                if (i < total) wh_att[i] = v[k];  // kst, vst, kss, vss are contiguous in this order
+            }
+        }
+    }
+    __syncthreads();
     const int item = blockIdx.x * kWhWarps + warp;
-    if (item >= frames * heads) return;
-    float *sc = wh_scores + (size_t)warp * frames;
-    const int t = item / heads, h = item - t * heads;
-    const int group = heads / kv, kh = h / group, words = qk / 4;
-    // the query as int32 words (qk % 4 == 0, rows on 4-byte boundaries): the
-    // int dot by dp4a, the same exact int32 as the byte loop
+    if (item >= frames * group) return;
+    float *sc = scores + (size_t)warp * frames;
+    const int t = item / group, h = kh * group + (item - (item / group) * group);
+    // the query as int32 words (qk % 4 == 0): dp4a gives the same exact int32 dot
     int qw[kWhMaxHead / 4];
     const int *qrow = reinterpret_cast<const int *>(q8 + (size_t)t * heads * qk + h * qk);
 #pragma unroll
-    for (int i = 0; i < kWhMaxHead / 4; i++) qw[i] = i < words ? qrow[i] : 0;
+    for (int i = 0; i < kWhMaxHead / 4; i++) qw[i] = i < kwords ? qrow[i] : 0;
     const float scale = __fmul_rn(qs[(size_t)t * heads + h], inv_sqrt);
     float peak = -INFINITY;
     for (int j = lane; j < frames; j += 32) {
-        const int *kr = reinterpret_cast<const int *>(keys + (size_t)j * kv * qk + kh * qk);
+        const int *kr = kst + (size_t)j * kwords;
         int dot = 0;
 #pragma unroll
         for (int i = 0; i < kWhMaxHead / 4; i++)
-            if (i < words) dot = __dp4a(kr[i], qw[i], dot);
-        const float s = __fmul_rn(__fmul_rn(__int2float_rn(dot), ks[(size_t)j * kv + kh]), scale);
+            if (i < kwords) dot = __dp4a(kr[i], qw[i], dot);
+        const float s = __fmul_rn(__fmul_rn(__int2float_rn(dot), kss[j]), scale);
         sc[j] = s;
         peak = fmaxf(peak, s);
     }
@@ -426,26 +503,39 @@ __global__ void __launch_bounds__(32 * kWhWarps) wh_attention_kernel(
     if (lane == 0)
         for (int j = 0; j < frames; j++) total = __fadd_rn(total, sc[j]);
     total = __shfl_sync(0xffffffffu, total, 0);
-    // p_j = e_j / total, then the PV weight p_j * vs_j, both per position
-    for (int j = lane; j < frames; j += 32) sc[j] = __fmul_rn(__fdiv_rn(sc[j], total), vs[(size_t)j * kv + kh]);
+    // p_j = e_j / total, then the PV weight p_j * vs_j
+    for (int j = lane; j < frames; j += 32) sc[j] = __fmul_rn(__fdiv_rn(sc[j], total), vss[j]);
     __syncwarp();
-    const int8_t *vbase = values + kh * vd;
-    const size_t vstride = (size_t)kv * vd;
-    for (int d = lane; d < vd; d += 32) {
-        float acc = 0.0f;
-        int j = 0;
-        for (; j + 4 <= frames; j += 4) {
-            float v[4], wj[4];
+    const int8_t *vb = reinterpret_cast<const int8_t *>(vst);
+    const int d0 = lane, d1 = lane + 32;
+    const bool has0 = d0 < vd, has1 = d1 < vd;
+    float a0 = 0.0f, a1 = 0.0f;
+    int j = 0;
+    for (; j + 8 <= frames; j += 8) {
+        float w8[8], v0[8], v1[8];
 #pragma unroll
-            for (int u = 0; u < 4; u++) {
-                v[u] = (float)vbase[(size_t)(j + u) * vstride + d];
-                wj[u] = sc[j + u];
-            }
-#pragma unroll
-            for (int u = 0; u < 4; u++) acc = __fadd_rn(acc, __fmul_rn(wj[u], v[u]));
+        for (int u = 0; u < 8; u++) {
+            w8[u] = sc[j + u];
+            v0[u] = has0 ? (float)vb[(size_t)(j + u) * vd + d0] : 0.0f;
+            v1[u] = has1 ? (float)vb[(size_t)(j + u) * vd + d1] : 0.0f;
         }
-        for (; j < frames; j++) acc = __fadd_rn(acc, __fmul_rn(sc[j], (float)vbase[(size_t)j * vstride + d]));
-        out[(size_t)t * heads * vd + h * vd + d] = acc;
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+            a0 = __fadd_rn(a0, __fmul_rn(w8[u], v0[u]));
+            a1 = __fadd_rn(a1, __fmul_rn(w8[u], v1[u]));
+        }
+    }
+    for (; j < frames; j++) {
+        a0 = __fadd_rn(a0, __fmul_rn(sc[j], has0 ? (float)vb[(size_t)j * vd + d0] : 0.0f));
+        a1 = __fadd_rn(a1, __fmul_rn(sc[j], has1 ? (float)vb[(size_t)j * vd + d1] : 0.0f));
+    }
+    float *o = out + (size_t)t * heads * vd + h * vd;
+    if (has0) o[d0] = a0;
+    if (has1) o[d1] = a1;
+    for (int d = lane + 64; d < vd; d += 32) {  // v dims past 64 (not taken by the encoder's checks)
+        float acc = 0.0f;
+        for (int jj = 0; jj < frames; jj++) acc = __fadd_rn(acc, __fmul_rn(sc[jj], (float)vb[(size_t)jj * vd + d]));
+        o[d] = acc;
     }
 }
 
@@ -533,6 +623,12 @@ __global__ void __launch_bounds__(32 * kWhWarps) wh_cross_quant_kernel(
 
 unsigned wh_blocks(long long threads, int per_block) { return (unsigned)((threads + per_block - 1) / per_block); }
 
+// wh_attention_kernel's shared memory: keys and values of every frame, their
+// scales, and kWhWarps score rows.
+size_t wh_attention_smem(int frames, int qk, int vd) {
+    return (size_t)frames * (qk + vd) + (size_t)frames * 4 * (2 + kWhWarps);
+}
+
 }  // namespace
 }  // namespace ndl
 
@@ -583,6 +679,7 @@ struct ndl_whistle {
     int32_t *bitrev, *mel_first, *mel_count, *mel_lo, *mel_hi;
     double *col_mean, *col_den;
     unsigned *peak;
+    int *status;  // kStatusTimeout when a bounded wait ran out
     float *padded, *mel, *stage0, *dw, *pw, *flat, *stem_out, *stream_a, *stream_b, *u, *residual, *pre, *post, *res,
         *hpre, *post_gate, *mix_logits, *mix, *quarters, *q, *k, *v, *gate, *qs, *ks, *vs, *attn_out, *proj, *glu,
         *hidden, *conv, *gate_rows, *enc_out, *cross_rows, *cross_k, *cross_v;
@@ -852,8 +949,9 @@ int whistle_buffers(ndl_whistle *w) {
     const size_t tokens = std::max(stem_tokens, F);
     w->act_stride = (int)((cols / 128 + 7) & ~(size_t)7);
     WH_TRY(whistle_buf(w, &w->peak, 1));
+    WH_TRY(whistle_buf(w, &w->status, 1));
     WH_TRY(whistle_buf(w, &w->padded, (size_t)w->window + w->max_samples + w->hop + w->fft));
-    WH_TRY(whistle_buf(w, &w->mel, (size_t)w->max_l0 * w->mels));
+    WH_TRY(whistle_buf(w, &w->mel, (size_t)w->max_l0 * w->mels + 4));  // + 4: the bulk copies round up to 16 bytes
     WH_TRY(whistle_buf(w, &w->stage0, (size_t)w->max_l1 * 40 * s));
     WH_TRY(whistle_buf(w, &w->dw, stem_tokens * s));
     WH_TRY(whistle_buf(w, &w->pw, stem_tokens * s));
@@ -941,6 +1039,7 @@ int whistle_run(ndl_whistle *w, int samples) {
     const int E = w->encoder_layers;
     // front end
     NDL_CUDA(cudaMemsetAsync(w->peak, 0, sizeof(unsigned), st));
+    NDL_CUDA(cudaMemsetAsync(w->status, 0, sizeof(int), st));
     launch_kernel(wh_mel_kernel, dim3((unsigned)l0), dim3(256), (size_t)(2 * fft + fft / 2 + 1) * 4, st, w->padded,
                   hop, fft, window, w->hann, w->cosines, w->sines, w->bitrev, w->bank, mels, w->mel_first,
                   w->mel_count, w->mel_lo, w->mel_hi, w->mel, w->peak);
@@ -948,8 +1047,17 @@ int whistle_run(ndl_whistle *w, int samples) {
     const long long nmel = (long long)l0 * mels;
     launch_kernel(wh_log_kernel, dim3(wh_blocks(nmel, 256)), dim3(256), 0, st, w->mel, nmel, (const unsigned *)w->peak);
     WH_LAUNCH("wh_log");
-    launch_kernel(wh_moments_kernel, dim3(wh_blocks(mels, 32)), dim3(32), 0, st, (const float *)w->mel, l0, mels,
-                  w->col_mean, w->col_den);
+    {
+        const size_t smem = (size_t)2 * kMomRows * mels * 4;
+        static DeviceOnce smem_attribute;
+        WH_TRY(smem_attribute.run([] {
+            const cudaError_t e = cudaFuncSetAttribute(wh_moments_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                       2 * kMomRows * 128 * 4);
+            return e == cudaSuccess ? (int)NDL_OK : set_error(NDL_ERR_CUDA, "wh_moments smem: %s", cudaGetErrorString(e));
+        }));
+        launch_kernel(wh_moments_kernel, dim3(1), dim3(128), smem, st, (const float *)w->mel, l0, mels, w->col_mean,
+                      w->col_den, w->status);
+    }
     WH_LAUNCH("wh_moments");
     launch_kernel(wh_standardize_kernel, dim3(wh_blocks(nmel, 256)), dim3(256), 0, st, w->mel, nmel, mels,
                   (const double *)w->col_mean, (const double *)w->col_den);
@@ -1017,10 +1125,20 @@ int whistle_run(ndl_whistle *w, int samples) {
                       L.k_norm, (const float *)w->rope_cos, (const float *)w->rope_sin, w->q8, w->qs, w->keys, w->ks,
                       w->values, w->vs);
         WH_LAUNCH("wh_qkv");
-        launch_kernel(wh_attention_kernel, dim3(wh_blocks((long long)F * H, kWhWarps)), dim3(32 * kWhWarps),
-                      (size_t)kWhWarps * F * 4, st, (const int8_t *)w->q8, (const float *)w->qs, F, H, KV, QK, VD,
-                      inv_sqrt, (const int8_t *)w->keys, (const float *)w->ks, (const int8_t *)w->values,
-                      (const float *)w->vs, w->attn_out);
+        static DeviceOnce attention_smem;
+        WH_TRY(attention_smem.run([] {
+            int dev = 0, optin = 0;
+            cudaGetDevice(&dev);
+            cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+            const cudaError_t e =
+                cudaFuncSetAttribute(wh_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, optin);
+            return e == cudaSuccess ? (int)NDL_OK
+                                    : set_error(NDL_ERR_CUDA, "wh_attention smem: %s", cudaGetErrorString(e));
+        }));
+        launch_kernel(wh_attention_kernel, dim3(wh_blocks((long long)F * (H / KV), kWhWarps), (unsigned)KV),
+                      dim3(32 * kWhWarps), wh_attention_smem(F, QK, VD), st, (const int8_t *)w->q8,
+                      (const float *)w->qs, F, H, KV, QK, VD, inv_sqrt, (const int8_t *)w->keys, (const float *)w->ks,
+                      (const int8_t *)w->values, (const float *)w->vs, w->attn_out);
         WH_LAUNCH("wh_attention");
         WH_TRY(wh_row_prepare(w, 2, false, w->attn_out, w->gate, F, H * VD, 2));
         WH_TRY(wh_matmul(w, L.out, F, w->proj));
@@ -1098,7 +1216,7 @@ extern "C" NDL_API int ndl_whistle_create(const ndl_model *m, int max_samples, n
     const int d = info.dim;
     int rc = NDL_OK;
     if (stages != 3) rc = set_error(NDL_ERR_UNSUPPORTED, "three-stage stem expected, the manifest says %d", stages);
-    else if (E < 1 || conv < 1 || w->mels < 1 || w->hop < 1 || w->window < 2 || w->fft < 2 || w->fft > kWhMaxFft ||
+    else if (E < 1 || conv < 1 || w->mels < 1 || w->mels > 128 || w->hop < 1 || w->window < 2 || w->fft < 2 || w->fft > kWhMaxFft ||
              (w->fft & (w->fft - 1)) != 0 || w->window > w->fft || w->rate < 1)
         rc = set_error(NDL_ERR_UNSUPPORTED, "audio manifest: %d layers, kernel %d, %d mels, fft %d, window %d, hop %d",
                        E, conv, w->mels, w->fft, w->window, w->hop);
@@ -1151,6 +1269,9 @@ extern "C" NDL_API int ndl_whistle_encode(ndl_whistle *w, const float *pcm, int 
     const int rc = ndl_whistle_encode_device(w, pcm, samples);
     if (rc != NDL_OK) return rc;
     NDL_CUDA(cudaStreamSynchronize(w->stream));
+    int status = 0;
+    NDL_CUDA(cudaMemcpy(&status, w->status, sizeof(int), cudaMemcpyDeviceToHost));
+    if (status) return set_error(NDL_ERR_TIMEOUT, "whistle encode: a bounded wait ran out (status %d)", status);
     *frames = w->frames;
     return NDL_OK;
 }
