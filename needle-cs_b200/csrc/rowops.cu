@@ -604,6 +604,40 @@ __device__ __forceinline__ void mlp_batched(int n, int tid, int threads, Load lo
     }
 }
 
+// The ascending fp32 sum of x[0..n) (shared memory, 16-byte aligned) on one
+// thread, its next four float4 loads issued ahead of the current adds.
+__device__ __forceinline__ float mlp_ordered_sum(const float *x, int n) {
+    float sum = 0.0f;
+    if ((reinterpret_cast<uintptr_t>(x) & 15) != 0) {  // rows of a width that is not a multiple of 4
+        for (int i = 0; i < n; i++) sum = __fadd_rn(sum, x[i]);
+        return sum;
+    }
+    const int nv = n >> 2;
+    const float4 *v = reinterpret_cast<const float4 *>(x);
+    const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+    float4 nxt[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) nxt[j] = j < nv ? v[j] : zero;
+    for (int i = 0; i < nv; i += 4) {
+        float4 cur[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            cur[j] = nxt[j];
+            nxt[j] = i + 4 + j < nv ? v[i + 4 + j] : zero;
+        }
+#pragma unroll
+        for (int j = 0; j < 4; j++)
+            if (i + j < nv) {
+                sum = __fadd_rn(sum, cur[j].x);
+                sum = __fadd_rn(sum, cur[j].y);
+                sum = __fadd_rn(sum, cur[j].z);
+                sum = __fadd_rn(sum, cur[j].w);
+            }
+    }
+    for (int i = nv * 4; i < n; i++) sum = __fadd_rn(sum, x[i]);
+    return sum;
+}
+
 struct MlpCondition {
     float w[8], d2, b2;
     int perm;
@@ -631,9 +665,7 @@ __global__ void __launch_bounds__(256) slot_hadamard_mlp_kernel(KtMlpArgs a) {
     });
     __syncthreads();
     if (tid == 0) {  // the sum of squares in order
-        float sum = 0.0f;
-#pragma unroll 16
-        for (int i = 0; i < dim; i++) sum = __fadd_rn(sum, scratch[i]);
+        const float sum = mlp_ordered_sum(scratch, dim);
         weights[0] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, (float)dim), 1e-6f)));
     } else if (tid >= 32) {  // meanwhile the other warps stage the Kronecker factors
         const int sizes[6] = {input_rows * rows, cols * cols, rows * rows, cols * cols, rows * rows, cols * cols};
@@ -666,25 +698,25 @@ __global__ void __launch_bounds__(256) slot_hadamard_mlp_kernel(KtMlpArgs a) {
         normalized[i] = __fmul_rn(__fmul_rn(__fadd_rn(1.0f, p), res[i]), inv);
     });
     __syncthreads();
-    // ConditionWeights: products in parallel, weight j summed in order by thread j
+    // ConditionWeights: products in parallel (weight j's row of dim contiguous),
+    // weight j summed in order by thread j
     mlp_batched<8>(dim * 8, tid, nt, [&](int e) { return __ldg(cond_v + e); },
-                   [&](int e, float w) { scratch[e] = __fmul_rn(normalized[e >> 3], w); });
+                   [&](int e, float w) { scratch[(e & 7) * dim + (e >> 3)] = __fmul_rn(normalized[e >> 3], w); });
     __syncthreads();
+    if (tid < 8) weights[tid] = mlp_ordered_sum(scratch + tid * dim, dim);
+    __syncthreads();
+    // Softmax over the 8 weights: the peak and the exponentials on 8 threads, the
+    // total in order and the divisions on thread 0
     if (tid < 8) {
-        float sum = 0.0f;
-#pragma unroll 16
-        for (int i = 0; i < dim; i++) sum = __fadd_rn(sum, scratch[i * 8 + tid]);
-        weights[tid] = sum;
+        float peak = -INFINITY;
+        for (int j = 0; j < 8; j++) peak = fmaxf(peak, weights[j]);
+        scratch[tid] = exp_rn(__fsub_rn(weights[tid], peak));
     }
     __syncthreads();
-    if (tid == 0) {  // Softmax over the 8 weights
-        float peak = -INFINITY, total = 0.0f;
-        for (int j = 0; j < 8; j++) peak = fmaxf(peak, weights[j]);
-        for (int j = 0; j < 8; j++) {
-            weights[j] = exp_rn(__fsub_rn(weights[j], peak));
-            total = __fadd_rn(total, weights[j]);
-        }
-        for (int j = 0; j < 8; j++) weights[j] = __fdiv_rn(weights[j], total);
+    if (tid == 0) {
+        float total = 0.0f;
+        for (int j = 0; j < 8; j++) total = __fadd_rn(total, scratch[j]);
+        for (int j = 0; j < 8; j++) weights[j] = __fdiv_rn(scratch[j], total);
     }
     mlp_batched<4>(input_rows * cols, tid, nt, [&](int i) { return i < dim ? __ldg(d1 + i) : 0.0f; },
                    [&](int i, float w) { front[i] = i < dim ? __fmul_rn(normalized[i], w) : 0.0f; });

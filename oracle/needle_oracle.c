@@ -165,20 +165,19 @@ static float exp_rn(float x) {
     const double xd = (double)x;
     const double k = rint(xd * 1.4426950408889634);
     const double r = (xd - k * 6.93147180369123816490e-01) - k * 1.90821492927058770002e-10;
-    double p = 1.6059043836821614599e-10;      /* 1/13! */
-    p = fma(p, r, 2.0876756987868098979e-09); /* 1/12! */
-    p = fma(p, r, 2.5052108385441718775e-08); /* 1/11! */
-    p = fma(p, r, 2.7557319223985890653e-07); /* 1/10! */
-    p = fma(p, r, 2.7557319223985890653e-06); /* 1/9! */
-    p = fma(p, r, 2.4801587301587301587e-05); /* 1/8! */
-    p = fma(p, r, 1.9841269841269841270e-04); /* 1/7! */
-    p = fma(p, r, 1.3888888888888888889e-03); /* 1/6! */
-    p = fma(p, r, 8.3333333333333333333e-03); /* 1/5! */
-    p = fma(p, r, 4.1666666666666666667e-02); /* 1/4! */
-    p = fma(p, r, 1.6666666666666666667e-01); /* 1/3! */
-    p = fma(p, r, 0.5);
-    p = fma(p, r, 1.0);
-    p = fma(p, r, 1.0);
+    /* the degree-13 Taylor polynomial by Estrin's scheme (pairs, then r^2, r^4,
+     * r^8 levels): four dependent fused steps instead of thirteen */
+    const double r2 = r * r, r4 = r2 * r2, r8 = r4 * r4;
+    const double q0 = fma(1.0, r, 1.0);                                            /* 1 + r */
+    const double q1 = fma(1.6666666666666666667e-01, r, 0.5);                      /* 1/2! + r/3! */
+    const double q2 = fma(8.3333333333333333333e-03, r, 4.1666666666666666667e-02); /* 1/4!, 1/5! */
+    const double q3 = fma(1.9841269841269841270e-04, r, 1.3888888888888888889e-03); /* 1/6!, 1/7! */
+    const double q4 = fma(2.7557319223985890653e-06, r, 2.4801587301587301587e-05); /* 1/8!, 1/9! */
+    const double q5 = fma(2.5052108385441718775e-08, r, 2.7557319223985890653e-07); /* 1/10!, 1/11! */
+    const double q6 = fma(1.6059043836821614599e-10, r, 2.0876756987868098979e-09); /* 1/12!, 1/13! */
+    const double s0 = fma(q1, r2, q0), s1 = fma(q3, r2, q2), s2 = fma(q5, r2, q4);
+    const double t0 = fma(s1, r4, s0), t1 = fma(q6, r4, s2);
+    const double p = fma(t1, r8, t0);
     return (float)scalbn(p, (int)k);
 }
 
