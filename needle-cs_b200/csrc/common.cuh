@@ -152,7 +152,7 @@ __device__ __forceinline__ float sigmoid_simd(float x) {
 // Sinkhorn4x4, the Needle-3 gates, MLP and Engram): the float exponential
 // rounded to nearest, computed in double precision from the mathematics
 // (Cody and Waite's reduction with fdlibm's two-part ln 2, then the Taylor
-// series to degree 13), which equals the correctly rounded exp except within
+// series to degree 13 in Estrin's form), which equals the correctly rounded exp except within
 // about 1e-15 of a rounding midpoint.  Every double step is an explicit
 // IEEE operation, so the CPU oracle, which evaluates the same steps, returns
 // the same bits.

@@ -151,7 +151,7 @@ static float round_even(float x) {
  * IEEE operations only.  Cody and Waite's argument reduction x = k*ln2 + r,
  * k = rint(x/ln2), with ln2 split into a high part whose products with k are
  * exact and a low part (the split published with fdlibm); exp(r) by its
- * Taylor series to degree 13 in Horner form with fused multiply-adds; scaled
+ * Taylor series to degree 13 in Estrin's form with fused multiply-adds; scaled
  * by 2^k (exact) and rounded once to float.  The relative error before that
  * rounding is below 1e-15: the correctly rounded float unless exp(x) lies
  * within about 1e-15 of a rounding midpoint, where a C runtime's expf may
