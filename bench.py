@@ -1120,14 +1120,14 @@ def run_needle3(args, rank, world, local):
                                             "sites": list(g["sites"][:g["site_count"]]), "sessions_per_gpu": B,
                                             "prompt": P, "greedy": True, "weight_bytes": weights,
                                             "l2": "weights fit L2; each step reads them and every session's cache"},
-            "roofline": {"bound": "hbm", "kernel": "the whole step (launch- and latency-bound: 18 kernels per layer "
+            "roofline": {"bound": "hbm", "kernel": "the whole step (launch- and latency-bound: 11 kernels per layer "
                                                    "on 64 rows, replayed from a CUDA graph)",
                          "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak, "traffic": None,
                          "peak_source": peak_source, "algorithmic_bytes_per_step": step_bytes},
             "e2e": {"value": world * B * args.steps / wall, "unit": "tokens/s", "h2d_bytes_per_step": B * 12,
                     "d2h_bytes_per_step": B * 4},
-            # per step: 18 kernels a layer, 8 more at each Engram site, embedding 2, head 5, argmax 1
-            "gpu_launches": args.steps * (L * 18 + 8 * g["site_count"] + 8), "clocks": clocks.summary()}
+            # per step: 11 kernels a layer, 8 more at each Engram site, embedding 2, head 5, argmax 1
+            "gpu_launches": args.steps * (L * 11 + 8 * g["site_count"] + 8), "clocks": clocks.summary()}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         entry.load_oracle()
         line["cpu_baseline"] = needle3_cpu_sample(a)
@@ -1260,9 +1260,9 @@ def run_whistle(args, rank, world, local):
                          "traffic": None, "peak_source": peak_source, "algorithmic_bytes_per_step": weights},
             "e2e": {"value": world * WHISTLE_SECONDS * args.steps / (wall * 1e-3), "unit": "audio s/s",
                     "h2d_bytes_per_step": n * 4, "d2h_bytes_per_step": out.nbytes},
-            # per encode: front end 3, stem 11, lanes + fill 2, 23 a layer, final 2, cross rows and Prepare 2,
+            # per encode: front end 4, stem 11, lanes + fill 2, 20 a layer, final 2, cross rows and Prepare 2,
             # 2 per decoder layer
-            "gpu_launches": args.steps * (3 + 11 + 2 + 23 * E + 2 + 2 + 2 * L), "clocks": clocks.summary()}
+            "gpu_launches": args.steps * (4 + 11 + 2 + 20 * E + 2 + 2 + 2 * L), "clocks": clocks.summary()}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         entry.load_oracle()
         line["cpu_baseline"] = whistle_cpu_sample(a)

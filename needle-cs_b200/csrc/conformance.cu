@@ -54,15 +54,6 @@ struct KtTileArgs {
 };
 int launch_slot_attention_tile(const KtTileArgs &a, cudaStream_t stream);
 int launch_slot_merge_partials(const float *partials, int count, int heads, float *out, cudaStream_t stream);
-struct KtMlpArgs {
-    const float *w[13];
-    const float *pre_norm;
-    const int32_t *perm_a, *perm_b;
-    int dim, rows, cols;
-    float scale;
-    float *residual;
-};
-int launch_slot_hadamard_mlp(const KtMlpArgs &a, cudaStream_t stream);
 }  // namespace ndl
 
 namespace {

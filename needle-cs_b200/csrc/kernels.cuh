@@ -141,6 +141,34 @@ int launch_row_op(int mode, bool fake, const float *x, const float *aux, const f
 // n <= 4096 and x / aux sit on 16-byte boundaries.
 int launch_fake_a8_prepare(int mode, const float *x, const float *aux, int rows, int n, int bits, int8_t *values,
                            float *scales, float *offsets, int stride, cudaStream_t stream);
+// The hyper-connection prepare of a layer after its phi matmuls, CTA per
+// row: the pre / post gates and Sinkhorn logits of `layer` (pre, post [rows]
+// [ld] with the layer's 4 at 4 * layer, res with its 16 at 16 * layer), u =
+// Mix4(stream, hpre) also written to residual, mix = Sinkhorn4x4(logits).
+int launch_hc_prepare(const float *pre, int ld_pre, const float *post, int ld_post, const float *res, int ld_res,
+                      const float *a_pre, const float *b_pre, const float *a_post, const float *b_post,
+                      const float *a_res, const float *b_res, int layer, const float *stream, int dim, int rows, float *u,
+                      float *residual, float *post_gate, float *mix, cudaStream_t cs);
+// HadamardMlp.Apply's operands (block b works on row b).  Optional around
+// it, per row: a PostNormAdd before (pn_x non-null: residual += pn_gate[row]
+// ((1 + pn_scale) pn_x) InverseRms(pn_x)) and a CombineDiff4x4 after
+// (cb_next non-null: next lanes from the row's stream, mix, the final
+// residual, u and post gates).
+struct KtMlpArgs {
+    const float *w[13];
+    const float *pre_norm;
+    const int32_t *perm_a, *perm_b;
+    int dim, rows, cols;
+    float scale;
+    float *residual;
+    long long row_stride;  // block b updates residual + b * row_stride (0: one row)
+    const float *pn_x, *pn_scale, *pn_gate;
+    const float *cb_stream, *cb_mix, *cb_u, *cb_post;
+    float *cb_next;
+};
+int launch_slot_hadamard_mlp(const KtMlpArgs &a, cudaStream_t stream);
+// The same kernel over `count` rows (a.row_stride apart).
+int launch_mlp_rows(const KtMlpArgs &a, int count, cudaStream_t stream);
 // HadamardMlp.Apply on `count` residual rows with explicit factors (d1, d2,
 // b2, d3, d4, w1a, w1b, w2a, w2b, w3a, w3b, cond_v, cond_u), block per row.
 int launch_hadamard_mlp_rows(const float *const w[13], const float *pre_norm, const int32_t *perm_a,

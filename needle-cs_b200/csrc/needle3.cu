@@ -54,6 +54,7 @@ struct LayerView {
     const float *norm_in, *q_taps, *k_taps, *v_taps, *q_norm, *k_norm, *post_norm;
     float attn_gate;  // sigmoid of the stored logit
     int window;       // 0: global
+    const float *mlp[13], *pre_hada;  // HadamardMlp factors (d1 .. cond_u) and pre-norm scale
 };
 
 }  // namespace
@@ -80,7 +81,9 @@ struct N3State {
     int32_t *d_rows = nullptr;  // tokens, slots, heads [max_rows] each
     int32_t *h_rows = nullptr;  // pinned staging
     float *gathered, *stream, *next, *u, *residual, *norm4, *pre, *post, *res, *hpre, *post_gate, *mix_logits, *mix;
-    float *quarters, *gate_rows, *q, *k, *v, *gate, *triples, *qc, *kc, *vc, *attn_out, *proj, *mean, *headn;
+    const int32_t *perm_a = nullptr, *perm_b = nullptr;  // the model's HadamardMlp permutations (device)
+    int hada_rows = 0, hada_cols = 0;
+    float *quarters, *gate_rows, *q, *k, *v, *gate, *qc, *kc, *vc, *attn_out, *proj, *mean, *headn;
     float *head_logits;  // [max_heads][vocab] of one wave
     int8_t *act_values = nullptr, *q8 = nullptr;
     float *act_scales = nullptr, *act_offsets = nullptr, *qs = nullptr;
@@ -148,41 +151,17 @@ __global__ void n3_embed_kernel(const float *__restrict__ x, int rows, int dim, 
     for (int l = 0; l < kLanes; l++) stream[((size_t)r * kLanes + l) * dim + c] = v;
 }
 
-// Hyper-connection gates of RunLayerBatch (src/Needle/Engine.cs:2366-2380),
-// one thread per row: hpre[i] = Sigmoid(a_pre[l] * pre[i] + b_pre[4l + i] +
-// (i == lane ? 4 : -4)), post_gate[i] = 2 Sigmoid(a_post[l] * post[i] +
-// b_post[4l + i] + (i == lane ? 0 : -4)), logits[j] = a_res[l] * res[j] +
-// b_res[16l + j]; each sum left to right, one rounding per operation.
-__global__ void n3_gates_kernel(const float *__restrict__ pre, int ld_pre, const float *__restrict__ post, int ld_post,
-                                const float *__restrict__ res, int ld_res, const float *__restrict__ a_pre,
-                                const float *__restrict__ b_pre, const float *__restrict__ a_post,
-                                const float *__restrict__ b_post, const float *__restrict__ a_res,
-                                const float *__restrict__ b_res, int layer, int rows, float *__restrict__ hpre,
-                                float *__restrict__ post_gate, float *__restrict__ logits) {
-    pdl_enter();
-    const int t = blockIdx.x * blockDim.x + threadIdx.x;
-    if (t >= rows) return;
-    const int lane = layer % kLanes;
-    const float *pr = pre + (size_t)t * ld_pre + layer * kLanes, *po = post + (size_t)t * ld_post + layer * kLanes;
-    const float *rr = res + (size_t)t * ld_res + layer * 16;
-    for (int i = 0; i < kLanes; i++) {
-        const float zp = __fadd_rn(__fadd_rn(__fmul_rn(a_pre[layer], pr[i]), b_pre[layer * kLanes + i]),
-                                   i == lane ? 4.0f : -4.0f);
-        hpre[t * kLanes + i] = sigmoid_rn(zp);
-        const float zq = __fadd_rn(__fadd_rn(__fmul_rn(a_post[layer], po[i]), b_post[layer * kLanes + i]),
-                                   i == lane ? 0.0f : -4.0f);
-        post_gate[t * kLanes + i] = __fmul_rn(2.0f, sigmoid_rn(zq));
-    }
-    for (int j = 0; j < 16; j++) logits[t * 16 + j] = __fadd_rn(__fmul_rn(a_res[layer], rr[j]), b_res[layer * 16 + j]);
-}
-
-// The 3-tap conv inputs (ChainTriple, src/Needle/Engine.cs:2471-2478): per
-// row the triple (x_{t-2}, x_{t-1}, x_t) of each projection from the slot's
-// two previous ones, which then become (x_{t-1}, x_t).  Thread per (row,
-// column of q | k | v).
+// The 3-tap convs of the projections (ChainTriple, src/Needle/Engine.cs:
+// 2471-2478, and Scalar.Taps3, src/Needle/Scalar.cs:285-288): per row and
+// column of q | k | v, the triple (x_{t-2}, x_{t-1}, x_t) from the slot's two
+// previous projections, out = taps[c] x_t + taps[w + c] x_{t-1} + taps[2w + c]
+// x_{t-2} in that order, and the history becomes (x_{t-1}, x_t).  Thread per
+// (row, column).
 __global__ void n3_conv_kernel(const float *__restrict__ q, const float *__restrict__ k, const float *__restrict__ v,
                                const int32_t *__restrict__ row_slots, int rows, int layer, int layers, int qw, int kw,
-                               int vw, float *__restrict__ hist, float *__restrict__ triples) {
+                               int vw, const float *__restrict__ q_taps, const float *__restrict__ k_taps,
+                               const float *__restrict__ v_taps, float *__restrict__ hist, float *__restrict__ qc,
+                               float *__restrict__ kc, float *__restrict__ vc) {
     pdl_enter();
     const int width = qw + kw + vw;
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
@@ -192,21 +171,20 @@ __global__ void n3_conv_kernel(const float *__restrict__ q, const float *__restr
     float *h = hist + ((size_t)slot * layers + layer) * kConvHist * width;
     float cur;
     int w, cc;
-    float *tri;
+    const float *taps;
+    float *dst;
     if (c < qw) {
-        cur = q[(size_t)r * qw + c], w = qw, cc = c, tri = triples;
+        cc = c, cur = q[(size_t)r * qw + cc], w = qw, taps = q_taps, dst = qc + (size_t)r * qw;
     } else if (c < qw + kw) {
-        cc = c - qw, cur = k[(size_t)r * kw + cc], w = kw, tri = triples + (size_t)rows * 3 * qw;
+        cc = c - qw, cur = k[(size_t)r * kw + cc], w = kw, taps = k_taps, dst = kc + (size_t)r * kw;
     } else {
-        cc = c - qw - kw, cur = v[(size_t)r * vw + cc], w = vw, tri = triples + (size_t)rows * 3 * (qw + kw);
+        cc = c - qw - kw, cur = v[(size_t)r * vw + cc], w = vw, taps = v_taps, dst = vc + (size_t)r * vw;
     }
     // history layout per slot and layer: [2][q | k | v] as QkvOf (q history both entries, then k, then v)
     float *hq = h + (c < qw ? 0 : c < qw + kw ? kConvHist * qw : kConvHist * (qw + kw));
     const float h0 = hq[cc], h1 = hq[w + cc];
-    float *out = tri + (size_t)r * 3 * w;
-    out[cc] = h0;
-    out[w + cc] = h1;
-    out[2 * w + cc] = cur;
+    const float acc = __fadd_rn(__fmul_rn(taps[cc], cur), __fmul_rn(taps[w + cc], h1));
+    dst[cc] = __fadd_rn(acc, __fmul_rn(taps[2 * w + cc], h0));
     hq[cc] = h1;
     hq[w + cc] = cur;
 }
@@ -468,14 +446,9 @@ int forward_wave(N3State *s, const int32_t *tokens, const int32_t *slots, const 
                 cq_job(s->phi_res, l * 16, l * 16 + 16, s->res, s->phi_res.rows)};
             N3_TRY(cq_matmuls(s, R, views, jobs, 3, st));
         }
-        launch_kernel(n3_gates_kernel, dim3((R + 127) / 128), dim3(128), 0, st, (const float *)s->pre,
-                      s->phi_pre.rows, (const float *)s->post, s->phi_post.rows, (const float *)s->res,
-                      s->phi_res.rows, s->a_pre,
-                      s->b_pre, s->a_post, s->b_post, s->a_res, s->b_res, l, R, s->hpre, s->post_gate, s->mix_logits);
-        N3_TRY(check_launch("n3_gates"));
-        N3_TRY(ndl_hc_mix4(s->stream, d, s->hpre, R, s->u, st));
-        N3_TRY(ndl_hc_sinkhorn4x4(s->mix_logits, R, s->mix, st));
-        NDL_CUDA(cudaMemcpyAsync(s->residual, s->u, (size_t)R * d * 4, cudaMemcpyDeviceToDevice, st));
+        N3_TRY(launch_hc_prepare(s->pre, s->phi_pre.rows, s->post, s->phi_post.rows, s->res, s->phi_res.rows, s->a_pre,
+                                 s->b_pre, s->a_post, s->b_post, s->a_res, s->b_res, l, s->stream, d, R, s->u,
+                                 s->residual, s->post_gate, s->mix, st));
         // Engram
         const int site = s->site_of_layer[l];
         if (site >= 0) {
@@ -497,12 +470,10 @@ int forward_wave(N3State *s, const int32_t *tokens, const int32_t *slots, const 
         {
             const long long n = (long long)R * (s->qw + s->kw + s->vw);
             launch_kernel(n3_conv_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, st, s->q, s->k, s->v, slots,
-                          R, l, s->layers, s->qw, s->kw, s->vw, s->conv_hist, s->triples);
+                          R, l, s->layers, s->qw, s->kw, s->vw, L.q_taps, L.k_taps, L.v_taps, s->conv_hist, s->qc,
+                          s->kc, s->vc);
             N3_TRY(check_launch("n3_conv"));
         }
-        N3_TRY(ndl_taps3(L.q_taps, s->qw, s->triples, R, s->qc, st));
-        N3_TRY(ndl_taps3(L.k_taps, s->kw, s->triples + (size_t)R * 3 * s->qw, R, s->kc, st));
-        N3_TRY(ndl_taps3(L.v_taps, s->vw, s->triples + (size_t)R * 3 * (s->qw + s->kw), R, s->vc, st));
         {
             const int items = R * (s->heads + s->kv);
             launch_kernel(n3_qkv_post_kernel, dim3((items + kN3Warps - 1) / kN3Warps), dim3(32 * kN3Warps), 0, st,
@@ -532,11 +503,30 @@ int forward_wave(N3State *s, const int32_t *tokens, const int32_t *slots, const 
         }
         N3_TRY(fake_a8_prepare(s, 2, s->attn_out, s->gate, R, s->ow, L.out.bits, s->norm4, st));
         N3_TRY(cq_matmul(L.out, s, R, 0, d, s->proj, d, st));
-        // PostNormAdd(residual, proj, post_norm, sigmoid(attn_gate)): the layer's gate for every row
-        N3_TRY(ndl_fake_a8_rows(3, s->proj, L.post_norm, s->gate_rows + (size_t)l * s->max_rows, R, d, s->residual,
-                                st));
-        N3_TRY(ndl_mlp_apply(s->model, l, s->residual, R, 1.0f, st));
-        N3_TRY(ndl_hc_combine_diff4x4(s->stream, d, s->mix, s->residual, s->u, s->post_gate, R, s->next, st));
+        // one kernel per row: PostNormAdd(residual, proj, post_norm, sigmoid(attn_gate)) (the layer's gate
+        // for every row), the MLP, CombineDiff4x4 into the next streams
+        {
+            KtMlpArgs a{};
+            for (int k = 0; k < 13; k++) a.w[k] = L.mlp[k];
+            a.pre_norm = L.pre_hada;
+            a.perm_a = s->perm_a;
+            a.perm_b = s->perm_b;
+            a.dim = d;
+            a.rows = s->hada_rows;
+            a.cols = s->hada_cols;
+            a.scale = 1.0f;
+            a.residual = s->residual;
+            a.row_stride = d;
+            a.pn_x = s->proj;
+            a.pn_scale = L.post_norm;
+            a.pn_gate = s->gate_rows + (size_t)l * s->max_rows;
+            a.cb_stream = s->stream;
+            a.cb_mix = s->mix;
+            a.cb_u = s->u;
+            a.cb_post = s->post_gate;
+            a.cb_next = s->next;
+            N3_TRY(launch_mlp_rows(a, R, st));
+        }
         std::swap(s->stream, s->next);
     }
     launch_kernel(n3_advance_kernel, dim3((R + 127) / 128), dim3(128), 0, st, tokens, slots, R, s->prev, s->len);
@@ -848,6 +838,27 @@ int n3_create(const ndl_model *m, int slots, int capacity, int max_rows, int max
         v.attn_gate = 1.0f / (1.0f + host_exp_rn(-logit));  // Ops.Sigmoid's scalar form
         gates[l] = v.attn_gate;
         v.window = ((info.global_mask >> l) & 1) ? 0 : info.sliding_window;
+        static const char *mlp_names[13] = {"layer.mlp.d1",  "layer.mlp.d2",  "layer.mlp.b2",     "layer.mlp.d3",
+                                            "layer.mlp.d4",  "layer.mlp.w1a", "layer.mlp.w1b",    "layer.mlp.w2a",
+                                            "layer.mlp.w2b", "layer.mlp.w3a", "layer.mlp.w3b",    "layer.mlp.cond_v",
+                                            "layer.mlp.cond_u"};
+        const int hr = info.hada_rows, hc = info.hada_cols, hw = info.hada_n, in_rows = hc > 0 ? (d + hc - 1) / hc : 0;
+        const int64_t mlp_need[13] = {d, hw, hw, hw, d, (int64_t)in_rows * hr, (int64_t)hc * hc, (int64_t)hr * hr,
+                                      (int64_t)hc * hc, (int64_t)hr * hr, (int64_t)hc * hc, (int64_t)d * 8, 8LL * hw};
+        for (int k = 0; k < 13; k++)
+            if ((rc = dense_view(m, mlp_names[k], l, mlp_need[k], &v.mlp[k])) != NDL_OK) return fail(rc);
+        if ((rc = dense_view(m, "layer.pre_hada", l, d, &v.pre_hada)) != NDL_OK) return fail(rc);
+    }
+    {
+        ndl_model_tensor t;
+        if (ndl_model_get_tensor(m, "hyper.perm_a", 0, &t) != NDL_OK || t.count < info.hada_n) return fail(NDL_ERR_UNSUPPORTED);
+        s->perm_a = t.permutation;
+        if (ndl_model_get_tensor(m, "hyper.perm_b", 0, &t) != NDL_OK || t.count < info.hada_n) return fail(NDL_ERR_UNSUPPORTED);
+        s->perm_b = t.permutation;
+        s->hada_rows = info.hada_rows;
+        s->hada_cols = info.hada_cols;
+        if (info.hada_n <= 0 || (d + info.hada_cols - 1) / info.hada_cols > info.hada_rows)
+            return fail(set_error(NDL_ERR_UNSUPPORTED, "HadaN %d cannot hold a %d-wide row", info.hada_n, d));
     }
     s->site_of_layer.assign(L, -1);
     for (int i = 0; i < info.site_count; i++)
@@ -891,7 +902,6 @@ int n3_create(const ndl_model *m, int slots, int capacity, int max_rows, int max
         (rc = n3_alloc(s, &s->head_logits, (size_t)H * info.vocab)) != NDL_OK ||
         (rc = n3_alloc(s, &s->q, (size_t)R * s->qw)) != NDL_OK || (rc = n3_alloc(s, &s->k, (size_t)R * s->kw)) != NDL_OK ||
         (rc = n3_alloc(s, &s->v, (size_t)R * s->vw)) != NDL_OK || (rc = n3_alloc(s, &s->gate, (size_t)R * s->ow)) != NDL_OK ||
-        (rc = n3_alloc(s, &s->triples, (size_t)R * 3 * width)) != NDL_OK ||
         (rc = n3_alloc(s, &s->qc, (size_t)R * s->qw)) != NDL_OK || (rc = n3_alloc(s, &s->kc, (size_t)R * s->kw)) != NDL_OK ||
         (rc = n3_alloc(s, &s->vc, (size_t)R * s->vw)) != NDL_OK ||
         (rc = n3_alloc(s, &s->attn_out, (size_t)R * s->ow)) != NDL_OK ||

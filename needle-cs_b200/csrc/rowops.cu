@@ -16,6 +16,7 @@
 // through exp equals the scalar restatement bit for bit.
 #include "common.cuh"
 #include "cq.cuh"
+#include "hc.cuh"
 #include "kernels.cuh"
 
 namespace ndl {
@@ -63,33 +64,62 @@ __global__ void __launch_bounds__(256) combine4_kernel(const float *__restrict__
     dst[((size_t)t * kOut + o) * dim + c] = mix4_term(head, m[0], m[1], m[2], m[3], st, dim, c);
 }
 
-// Sinkhorn4x4 per token on 16 lanes, lane 4 * row + c holding entry (row, c):
-// each row and column sum gathers its four entries by shuffles and adds them
-// in index order, then every lane divides its own entry, so the steps and
-// roundings are the scalar loop's (Scalar.cs:361-381) with sixteen divides in
-// parallel.  Lanes past the last token run on zeros and store nothing.
+// Sinkhorn4x4 per token on 16 lanes (hc_sinkhorn16); lanes past the last
+// token run on zeros and store nothing.
 __global__ void __launch_bounds__(128) sinkhorn4x4_kernel(const float *__restrict__ logits, int n,
                                                           float *__restrict__ out) {
     pdl_enter();
     const long long gt = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     const long long t = gt >> 4;
-    const int lane = threadIdx.x & 31, base = lane & 16, e = lane & 15, row = e >> 2, c = e & 3;
+    const int lane = threadIdx.x & 31, e = lane & 15;
     const bool ok = t < n;
-    const float v = ok ? logits[t * 16 + e] : 0.0f;
-    const int rl = base + 4 * row;
-    const float peak = fmaxf(fmaxf(__shfl_sync(0xffffffffu, v, rl), __shfl_sync(0xffffffffu, v, rl + 1)),
-                             fmaxf(__shfl_sync(0xffffffffu, v, rl + 2), __shfl_sync(0xffffffffu, v, rl + 3)));
-    float r = exp_rn(__fsub_rn(v, peak));
-    for (int it = 0; it < 20; it++) {
-        const float a0 = __shfl_sync(0xffffffffu, r, rl), a1 = __shfl_sync(0xffffffffu, r, rl + 1);
-        const float a2 = __shfl_sync(0xffffffffu, r, rl + 2), a3 = __shfl_sync(0xffffffffu, r, rl + 3);
-        r = __fdiv_rn(r, __fadd_rn(__fadd_rn(__fadd_rn(a0, a1), a2), a3));
-        const float b0 = __shfl_sync(0xffffffffu, r, base + c), b1 = __shfl_sync(0xffffffffu, r, base + 4 + c);
-        const float b2 = __shfl_sync(0xffffffffu, r, base + 8 + c), b3 = __shfl_sync(0xffffffffu, r, base + 12 + c);
-        const float sum = __fadd_rn(__fadd_rn(__fadd_rn(b0, b1), b2), b3);
-        if (sum > 0.0f) r = __fdiv_rn(r, sum);
-    }
+    const float r = hc_sinkhorn16(ok ? logits[t * 16 + e] : 0.0f, lane);
     if (ok) out[t * 16 + e] = r;
+}
+
+// The hyper-connection prepare after the phi matmuls (RunLayerBatch,
+// src/Needle/Engine.cs:2366-2382; the encoder's ExecutePreHyper,
+// src/Needle/Whistle.cs:578-601), CTA per row: hpre[i] = Sigmoid(a_pre[l]
+// pre[i] + b_pre[4l + i] + (i == lane ? 4 : -4)), post_gate[i] = 2
+// Sigmoid(a_post[l] post[i] + b_post[4l + i] + (i == lane ? 0 : -4)) on
+// threads 0..3; the Sinkhorn logits a_res[l] res[j] + b_res[16l + j] on warp 1;
+// then u = Mix4(stream, hpre), also copied to the residual, and
+// mix = Sinkhorn4x4(logits) on warp 0.  Each sum left to right, one rounding
+// per operation.
+__global__ void __launch_bounds__(256) hc_prepare_kernel(
+    const float *__restrict__ pre, int ld_pre, const float *__restrict__ post, int ld_post,
+    const float *__restrict__ res, int ld_res, const float *__restrict__ a_pre, const float *__restrict__ b_pre,
+    const float *__restrict__ a_post, const float *__restrict__ b_post, const float *__restrict__ a_res,
+    const float *__restrict__ b_res, int layer, const float *__restrict__ stream, int dim, float *__restrict__ u,
+    float *__restrict__ residual, float *__restrict__ post_gate, float *__restrict__ mix) {
+    pdl_enter();
+    __shared__ float sh[4 + 16];
+    const int t = blockIdx.x, tid = threadIdx.x, lane = layer % 4;
+    if (tid < 4) {
+        const int i = tid;
+        const float *pr = pre + (size_t)t * ld_pre + layer * 4, *po = post + (size_t)t * ld_post + layer * 4;
+        const float zp = __fadd_rn(__fadd_rn(__fmul_rn(a_pre[layer], pr[i]), b_pre[layer * 4 + i]),
+                                   i == lane ? 4.0f : -4.0f);
+        sh[i] = sigmoid_rn(zp);
+        const float zq = __fadd_rn(__fadd_rn(__fmul_rn(a_post[layer], po[i]), b_post[layer * 4 + i]),
+                                   i == lane ? 0.0f : -4.0f);
+        post_gate[t * 4 + i] = __fmul_rn(2.0f, sigmoid_rn(zq));
+    } else if (tid >= 32 && tid < 48) {
+        const int j = tid - 32;
+        sh[4 + j] = __fadd_rn(__fmul_rn(a_res[layer], res[(size_t)t * ld_res + layer * 16 + j]), b_res[layer * 16 + j]);
+    }
+    __syncthreads();
+    const float w0 = sh[0], w1 = sh[1], w2 = sh[2], w3 = sh[3];
+    const float *st = stream + (size_t)t * 4 * dim;
+    for (int c = tid; c < dim; c += blockDim.x) {
+        const float x = hc_mix4(st, dim, c, w0, w1, w2, w3);
+        u[(size_t)t * dim + c] = x;
+        residual[(size_t)t * dim + c] = x;
+    }
+    if (tid < 32) {  // both half-warps hold the row's matrix; the first stores it
+        const float r = hc_sinkhorn16(sh[4 + (tid & 15)], tid);
+        if (tid < 16) mix[(size_t)t * 16 + tid] = r;
+    }
 }
 
 // Taps3 on triples [n][3][width] = (x_{t-2}, x_{t-1}, x_t).
@@ -518,16 +548,6 @@ int launch_slot_merge_partials(const float *partials, int count, int heads, floa
 // MlpWeights arrays (d1, d2, b2, d3, d4, w1a, w1b, w2a, w2b, w3a, w3b,
 // cond_v, cond_u); smem: weights[8], normalized[dim], front / back / kron
 // scratch [width] each.
-struct KtMlpArgs {
-    const float *w[13];
-    const float *pre_norm;
-    const int32_t *perm_a, *perm_b;
-    int dim, rows, cols;
-    float scale;
-    float *residual;
-    long long row_stride;  // block b updates residual + b * row_stride (0: one row)
-};
-
 // One Kronecker factor pair: tmp = left^T z (active_rows of z), then
 // result = tmp right, every element a sum in ascending index order.  Each
 // thread runs the chains of up to four elements (blockDim apart) side by
@@ -658,11 +678,36 @@ __global__ void __launch_bounds__(256) slot_hadamard_mlp_kernel(KtMlpArgs a) {
     const float *__restrict__ d3 = a.w[3], *__restrict__ d4 = a.w[4], *__restrict__ cond_v = a.w[11];
     const float *__restrict__ cond_u = a.w[12], *__restrict__ pre = a.pre_norm;
     const int32_t *__restrict__ perm_a = a.perm_a, *__restrict__ perm_b = a.perm_b;
-    // the residual row and its squares (ZeroCenteredRms)
-    mlp_batched<4>(dim, tid, nt, [&](int i) { return residual[i]; }, [&](int i, float r) {
-        res[i] = r;
-        scratch[i] = __fmul_rn(r, r);
-    });
+    if (a.pn_x) {
+        // Scalar.PostNormAdd first: the projection's squares summed in order, then
+        // residual + gate ((1 + scale) x) inverse, kept in res
+        const float *px = a.pn_x + (size_t)blockIdx.x * dim;
+        mlp_batched<4>(dim, tid, nt, [&](int i) { return px[i]; }, [&](int i, float x) {
+            normalized[i] = x;
+            scratch[i] = __fmul_rn(x, x);
+        });
+        __syncthreads();
+        if (tid == 0) {
+            const float sum = mlp_ordered_sum(scratch, dim);
+            weights[0] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, (float)dim), 1e-6f)));
+        }
+        __syncthreads();
+        const float pinv = weights[0], g = a.pn_gate[blockIdx.x];
+        const float *__restrict__ ps = a.pn_scale;
+        mlp_batched<4>(dim, tid, nt, [&](int i) { return make_float2(residual[i], __ldg(ps + i)); },
+                       [&](int i, float2 rs) {
+                           const float r = __fadd_rn(
+                               rs.x, __fmul_rn(g, __fmul_rn(__fmul_rn(__fadd_rn(1.0f, rs.y), normalized[i]), pinv)));
+                           res[i] = r;
+                           scratch[i] = __fmul_rn(r, r);
+                       });
+    } else {
+        // the residual row and its squares (ZeroCenteredRms)
+        mlp_batched<4>(dim, tid, nt, [&](int i) { return residual[i]; }, [&](int i, float r) {
+            res[i] = r;
+            scratch[i] = __fmul_rn(r, r);
+        });
+    }
     __syncthreads();
     if (tid == 0) {  // the sum of squares in order
         const float sum = mlp_ordered_sum(scratch, dim);
@@ -746,8 +791,34 @@ __global__ void __launch_bounds__(256) slot_hadamard_mlp_kernel(KtMlpArgs a) {
     __syncthreads();
     mlp_kron(front, rows, left3, right3, rows, cols, output_rows, tmp, back);
     mlp_batched<4>(dim, tid, nt, [&](int i) { return __ldg(d4 + i); }, [&](int i, float w) {
-        residual[i] = __fadd_rn(res[i], __fmul_rn(a.scale, __fmul_rn(back[i], w)));
+        const float r = __fadd_rn(res[i], __fmul_rn(a.scale, __fmul_rn(back[i], w)));
+        residual[i] = r;
+        res[i] = r;
     });
+    if (a.cb_next) {
+        // Ops.CombineDiff4x4 (Ops.cs:800-812) on the row: lane o of next =
+        // post[o] (residual - u) + mix[4o..4o+3] . stream, left to right
+        __syncthreads();
+        const size_t row = blockIdx.x;
+        const float *st = a.cb_stream + row * 4 * dim, *m = a.cb_mix + row * 16, *uu = a.cb_u + row * dim;
+        const float *pg = a.cb_post + row * 4;
+        float *nx = a.cb_next + row * 4 * dim;
+        for (int e = tid; e < 4 * dim; e += nt) {
+            const int o = e / dim, c = e - o * dim;
+            const float head = __fmul_rn(pg[o], __fsub_rn(res[c], uu[c]));
+            nx[e] = mix4_term(head, m[4 * o], m[4 * o + 1], m[4 * o + 2], m[4 * o + 3], st, dim, c);
+        }
+    }
+}
+
+int launch_mlp_rows(const KtMlpArgs &a, int count, cudaStream_t stream) {
+    if (count == 0) return NDL_OK;
+    const size_t smem = mlp_smem_floats(a.dim, a.rows, a.cols) * 4;
+    if (smem > 200 * 1024) return set_error(NDL_ERR_UNSUPPORTED, "hadamard_mlp: dim %d x width %d too large", a.dim,
+                                            a.rows * a.cols);
+    NDL_CUDA(cudaFuncSetAttribute(slot_hadamard_mlp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    launch_kernel(slot_hadamard_mlp_kernel, dim3((unsigned)count), dim3(256), smem, stream, a);
+    return check_launch("hadamard_mlp_rows");
 }
 
 int launch_hadamard_mlp_rows(const float *const w[13], const float *pre_norm, const int32_t *perm_a,
@@ -801,6 +872,15 @@ int launch_combine4(bool diff, const float *s, int dim, const float *mix, const 
         launch_kernel(combine4_kernel<false>, dim3(blocks_for((long long)n * dim, 256)), dim3(256), 0, stream, s, dim,
                       mix, x, u, post, n, dst);
     return check_launch("combine4");
+}
+int launch_hc_prepare(const float *pre, int ld_pre, const float *post, int ld_post, const float *res, int ld_res,
+                      const float *a_pre, const float *b_pre, const float *a_post, const float *b_post,
+                      const float *a_res, const float *b_res, int layer, const float *stream, int dim, int rows, float *u,
+                      float *residual, float *post_gate, float *mix, cudaStream_t cs) {
+    if (rows == 0) return NDL_OK;
+    launch_kernel(hc_prepare_kernel, dim3((unsigned)rows), dim3(256), 0, cs, pre, ld_pre, post, ld_post, res, ld_res,
+                  a_pre, b_pre, a_post, b_post, a_res, b_res, layer, stream, dim, u, residual, post_gate, mix);
+    return check_launch("hc_prepare");
 }
 int launch_sinkhorn4x4(const float *logits, int n, float *out, cudaStream_t stream) {
     if (n == 0) return NDL_OK;

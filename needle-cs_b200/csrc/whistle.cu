@@ -313,34 +313,6 @@ __global__ void wh_lanes_kernel(const float *__restrict__ stem, long long frames
     stream[i] = stem[t * dim + i % dim];
 }
 
-// ExecutePreHyper's scalars (Whistle.cs:578-601), thread per frame:
-// hpre = sigmoid(a_pre * pre + b_pre + (lane ? 4 : -4)), post gate =
-// 2 sigmoid(a_post * post + b_post + (lane ? 0 : -4)), Sinkhorn logits
-// a_res * res + b_res; and the Mix4 weights of the final mean (1/4 each).
-__global__ void wh_gates_kernel(const float *__restrict__ pre, const float *__restrict__ post,
-                                const float *__restrict__ res, const float *__restrict__ a_pre,
-                                const float *__restrict__ b_pre, const float *__restrict__ a_post,
-                                const float *__restrict__ b_post, const float *__restrict__ a_res,
-                                const float *__restrict__ b_res, int layer, int layers, int frames,
-                                float *__restrict__ hpre, float *__restrict__ post_gate, float *__restrict__ logits) {
-    pdl_enter();
-    const int t = blockIdx.x * blockDim.x + threadIdx.x;
-    if (t >= frames) return;
-    const int lane = layer % 4;
-    // pre / post [frames][4 layers], res [frames][16 layers]: the phi matmuls' full rows
-    const float *pr = pre + (size_t)t * 4 * layers + 4 * layer, *po = post + (size_t)t * 4 * layers + 4 * layer;
-    const float *rs = res + (size_t)t * 16 * layers + 16 * layer;
-    for (int i = 0; i < 4; i++) {
-        const float zp = __fadd_rn(__fadd_rn(__fmul_rn(a_pre[layer], pr[i]), b_pre[layer * 4 + i]),
-                                   i == lane ? 4.0f : -4.0f);
-        hpre[t * 4 + i] = sigmoid_rn(zp);
-        const float zq = __fadd_rn(__fadd_rn(__fmul_rn(a_post[layer], po[i]), b_post[layer * 4 + i]),
-                                   i == lane ? 0.0f : -4.0f);
-        post_gate[t * 4 + i] = __fmul_rn(2.0f, sigmoid_rn(zq));
-    }
-    for (int i = 0; i < 16; i++) logits[t * 16 + i] = __fadd_rn(__fmul_rn(a_res[layer], rs[i]), b_res[layer * 16 + i]);
-}
-
 __device__ __forceinline__ float wh_warp_max(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
@@ -681,7 +653,7 @@ struct ndl_whistle {
     unsigned *peak;
     int *status;  // kStatusTimeout when a bounded wait ran out
     float *padded, *mel, *stage0, *dw, *pw, *flat, *stem_out, *stream_a, *stream_b, *u, *residual, *pre, *post, *res,
-        *hpre, *post_gate, *mix_logits, *mix, *quarters, *q, *k, *v, *gate, *qs, *ks, *vs, *attn_out, *proj, *glu,
+        *post_gate, *mix, *quarters, *q, *k, *v, *gate, *qs, *ks, *vs, *attn_out, *proj, *glu,
         *hidden, *conv, *gate_rows, *enc_out, *cross_rows, *cross_k, *cross_v;
     int8_t *q8, *keys, *values;
     int8_t *act_values;
@@ -964,13 +936,12 @@ int whistle_buffers(ndl_whistle *w) {
     WH_TRY(whistle_buf(w, &w->stream_a, F * 4 * d));
     WH_TRY(whistle_buf(w, &w->stream_b, F * 4 * d));
     WH_TRY(whistle_buf(w, &w->glu, F * 2 * d));
-    float **f4[] = {&w->hpre, &w->post_gate, &w->quarters};
+    float **f4[] = {&w->post_gate, &w->quarters};
     for (float **p : f4) WH_TRY(whistle_buf(w, p, F * 4));
     const size_t E = w->encoder_layers;
     WH_TRY(whistle_buf(w, &w->pre, F * 4 * E));
     WH_TRY(whistle_buf(w, &w->post, F * 4 * E));
     WH_TRY(whistle_buf(w, &w->res, F * 16 * E));
-    WH_TRY(whistle_buf(w, &w->mix_logits, F * 16));
     WH_TRY(whistle_buf(w, &w->mix, F * 16));
     WH_TRY(whistle_buf(w, &w->gate_rows, F));
     WH_TRY(whistle_buf(w, &w->q, F * H * QK));
@@ -1105,13 +1076,9 @@ int whistle_run(ndl_whistle *w, int samples) {
                                     wh_job(w->phi_res, w->res, 16 * E, 16 * l, 16 * l + 16)};
         WH_TRY(launch_cq_matmul_jobs(phi, 3, 4 * d, 4, w->act_values, w->act_scales, w->act_offsets, w->act_stride, F,
                                      st));
-        launch_kernel(wh_gates_kernel, dim3(wh_blocks(F, 128)), dim3(128), 0, st, (const float *)w->pre,
-                      (const float *)w->post, (const float *)w->res, w->a_pre, w->b_pre, w->a_post, w->b_post,
-                      w->a_res, w->b_res, l, E, F, w->hpre, w->post_gate, w->mix_logits);
-        WH_LAUNCH("wh_gates");
-        WH_TRY(ndl_hc_mix4(stream, d, w->hpre, F, w->u, st));
-        WH_TRY(ndl_hc_sinkhorn4x4(w->mix_logits, F, w->mix, st));
-        NDL_CUDA(cudaMemcpyAsync(w->residual, w->u, (size_t)nd * 4, cudaMemcpyDeviceToDevice, st));
+        WH_TRY(launch_hc_prepare(w->pre, 4 * E, w->post, 4 * E, w->res, 16 * E, w->a_pre, w->b_pre, w->a_post,
+                                 w->b_post, w->a_res, w->b_res, l, stream, d, F, w->u, w->residual, w->post_gate,
+                                 w->mix, st));
         WH_TRY(launch_hadamard_mlp_rows(L.mlp0, L.pre_mlp_norm0, w->perm_a, w->perm_b, d, g.hada_rows, g.hada_cols,
                                         0.5f, w->residual, F, st));
         // RunSelfAttention (:840-862)
@@ -1160,9 +1127,25 @@ int whistle_run(ndl_whistle *w, int samples) {
         launch_kernel(wh_add_kernel, dim3(wh_blocks(nd, 256)), dim3(256), 0, st, w->residual, (const float *)w->proj,
                       nd);
         WH_LAUNCH("wh_add");
-        WH_TRY(launch_hadamard_mlp_rows(L.mlp, L.pre_mlp_norm, w->perm_a, w->perm_b, d, g.hada_rows, g.hada_cols, 0.5f,
-                                        w->residual, F, st));
-        WH_TRY(ndl_hc_combine_diff4x4(stream, d, w->mix, w->residual, w->u, w->post_gate, F, next, st));
+        {  // MLP, then CombineDiff4x4 into the next streams, one kernel per frame
+            KtMlpArgs a{};
+            for (int k = 0; k < 13; k++) a.w[k] = L.mlp[k];
+            a.pre_norm = L.pre_mlp_norm;
+            a.perm_a = w->perm_a;
+            a.perm_b = w->perm_b;
+            a.dim = d;
+            a.rows = g.hada_rows;
+            a.cols = g.hada_cols;
+            a.scale = 0.5f;
+            a.residual = w->residual;
+            a.row_stride = d;
+            a.cb_stream = stream;
+            a.cb_mix = w->mix;
+            a.cb_u = w->u;
+            a.cb_post = w->post_gate;
+            a.cb_next = next;
+            WH_TRY(launch_mlp_rows(a, F, st));
+        }
         std::swap(stream, next);
     }
     // ExecuteEncoderFinal (:614-626)
