@@ -301,14 +301,21 @@ __global__ void __launch_bounds__(32 * kN3Warps) n3_attention_kernel(
     const int slot = row_slots[r], p = len[slot];
     const int first = window == 0 ? 0 : max(0, p - window + 1);
     const int group = heads / kv, kh = h / group;
-    const int8_t *q = q8 + (size_t)r * heads * qk + h * qk;
+    // the query as int32 words (qk % 4 == 0, rows on 4-byte boundaries): dp4a gives the exact int32 dot
+    const int words = qk / 4;
+    int qw[16];
+    const int *qrow = reinterpret_cast<const int *>(q8 + (size_t)r * heads * qk + h * qk);
+#pragma unroll
+    for (int i = 0; i < 16; i++) qw[i] = i < words ? qrow[i] : 0;
     const float scale = __fmul_rn(qs[(size_t)r * heads + h], inv_sqrt);
     const size_t base = ((size_t)slot * layers + layer) * capacity;
     float peak = -INFINITY;
     for (int j = first + lane; j <= p; j += 32) {
-        const int8_t *kr = keys + (base + j) * kv * qk + kh * qk;
+        const int *kr = reinterpret_cast<const int *>(keys + (base + j) * kv * qk + kh * qk);
         int dot = 0;
-        for (int d = 0; d < qk; d++) dot += (int)q[d] * (int)kr[d];
+#pragma unroll
+        for (int i = 0; i < 16; i++)
+            if (i < words) dot = __dp4a(kr[i], qw[i], dot);
         const float s = __fmul_rn(__fmul_rn(__int2float_rn(dot), kscale[(base + j) * kv + kh]), scale);
         sc[j - first] = s;
         peak = fmaxf(peak, s);
@@ -321,16 +328,38 @@ __global__ void __launch_bounds__(32 * kN3Warps) n3_attention_kernel(
     if (lane == 0)
         for (int j = 0; j < count; j++) total = __fadd_rn(total, sc[j]);
     total = __shfl_sync(0xffffffffu, total, 0);
-    for (int j = lane; j < count; j += 32) sc[j] = __fdiv_rn(sc[j], total);
+    // p_j = e_j / total, then the PV weight p_j * vs_j, per position
+    for (int j = lane; j < count; j += 32)
+        sc[j] = __fmul_rn(__fdiv_rn(sc[j], total), vscale[(base + first + j) * kv + kh]);
     __syncwarp();
-    for (int d = lane; d < vd; d += 32) {
-        float acc = 0.0f;
-        for (int j = 0; j < count; j++) {
-            const size_t at = base + first + j;
-            const float w = __fmul_rn(sc[j], vscale[at * kv + kh]);
-            acc = __fadd_rn(acc, __fmul_rn(w, (float)values[at * kv * vd + kh * vd + d]));
+    const int8_t *vb = values + (base + first) * kv * vd + kh * vd;
+    const size_t vstride = (size_t)kv * vd;
+    for (int d0 = lane; d0 < vd; d0 += 64) {  // dims d0 and d0 + 32 side by side
+        const int d1 = d0 + 32;
+        const bool has1 = d1 < vd;
+        float a0 = 0.0f, a1 = 0.0f;
+        int j = 0;
+        for (; j + 8 <= count; j += 8) {
+            float w8[8], v0[8], v1[8];
+#pragma unroll
+            for (int u = 0; u < 8; u++) {
+                w8[u] = sc[j + u];
+                v0[u] = (float)vb[(size_t)(j + u) * vstride + d0];
+                v1[u] = has1 ? (float)vb[(size_t)(j + u) * vstride + d1] : 0.0f;
+            }
+#pragma unroll
+            for (int u = 0; u < 8; u++) {
+                a0 = __fadd_rn(a0, __fmul_rn(w8[u], v0[u]));
+                a1 = __fadd_rn(a1, __fmul_rn(w8[u], v1[u]));
+            }
         }
-        out[(size_t)r * heads * vd + h * vd + d] = acc;
+        for (; j < count; j++) {
+            a0 = __fadd_rn(a0, __fmul_rn(sc[j], (float)vb[(size_t)j * vstride + d0]));
+            if (has1) a1 = __fadd_rn(a1, __fmul_rn(sc[j], (float)vb[(size_t)j * vstride + d1]));
+        }
+        float *o = out + (size_t)r * heads * vd + h * vd;
+        o[d0] = a0;
+        if (has1) o[d1] = a1;
     }
 }
 
@@ -781,8 +810,9 @@ int n3_create(const ndl_model *m, int slots, int capacity, int max_rows, int max
     if (info.device < 0) return set_error(NDL_ERR_INVALID_ARG, "the model is not on a device");
     if (info.lanes != kLanes) return set_error(NDL_ERR_UNSUPPORTED, "%d hyper-connection lanes (4 supported)", info.lanes);
     if (info.conv_taps != 3) return set_error(NDL_ERR_UNSUPPORTED, "%d conv taps (3 supported)", info.conv_taps);
-    if (info.qk_dim > 64 || info.v_dim > 64 || info.qk_dim % 2 != 0)
-        return set_error(NDL_ERR_UNSUPPORTED, "head dims %d / %d (at most 64)", info.qk_dim, info.v_dim);
+    if (info.qk_dim > 64 || info.v_dim > 64 || info.qk_dim % 4 != 0)
+        return set_error(NDL_ERR_UNSUPPORTED, "head dims %d / %d (at most 64, qk a multiple of 4)", info.qk_dim,
+                         info.v_dim);
     if (info.kv_heads < 1 || info.heads % info.kv_heads != 0)
         return set_error(NDL_ERR_UNSUPPORTED, "%d heads over %d kv heads", info.heads, info.kv_heads);
     if (capacity < 1 || capacity > 8192) return set_error(NDL_ERR_UNSUPPORTED, "capacity %d (1..8192)", capacity);
