@@ -593,6 +593,45 @@ __device__ void mlp_kron(const float *z, int active_rows, const float *left, con
     __syncthreads();
 }
 
+// mlp_kron with each thread on four adjacent columns of one output row
+// (cols % 4 == 0, every array on 16-byte boundaries): per step one broadcast
+// load of the left (or tmp) value and one 16-byte load of z (or right) feed
+// four chains, the same products and sums in the same order.
+__device__ void mlp_kron4(const float *z, int active_rows, const float *left, const float *right, int rows, int cols,
+                          int result_rows, float *tmp, float *result) {
+    const int quads = cols >> 2, n = result_rows * quads;
+    for (int u = threadIdx.x; u < n; u += blockDim.x) {
+        const int k = u / quads, c = (u - k * quads) * 4;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+        for (int i = 0; i < active_rows; i++) {
+            const float l = left[i * rows + k];
+            const float4 zz = *reinterpret_cast<const float4 *>(z + i * cols + c);
+            acc.x = __fadd_rn(acc.x, __fmul_rn(l, zz.x));
+            acc.y = __fadd_rn(acc.y, __fmul_rn(l, zz.y));
+            acc.z = __fadd_rn(acc.z, __fmul_rn(l, zz.z));
+            acc.w = __fadd_rn(acc.w, __fmul_rn(l, zz.w));
+        }
+        *reinterpret_cast<float4 *>(tmp + k * cols + c) = acc;
+    }
+    __syncthreads();
+    for (int u = threadIdx.x; u < n; u += blockDim.x) {
+        const int k = u / quads, c = (u - k * quads) * 4;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+        for (int j = 0; j < cols; j++) {
+            const float t = tmp[k * cols + j];
+            const float4 rr = *reinterpret_cast<const float4 *>(right + j * cols + c);
+            acc.x = __fadd_rn(acc.x, __fmul_rn(t, rr.x));
+            acc.y = __fadd_rn(acc.y, __fmul_rn(t, rr.y));
+            acc.z = __fadd_rn(acc.z, __fmul_rn(t, rr.z));
+            acc.w = __fadd_rn(acc.w, __fmul_rn(t, rr.w));
+        }
+        *reinterpret_cast<float4 *>(result + k * cols + c) = acc;
+    }
+    __syncthreads();
+}
+
 // Shared floats of slot_hadamard_mlp_kernel: weights[8], normalized[dim],
 // front / back / tmp [width], scratch[8 * dim] (squares, then the
 // ConditionWeights products), the residual row [dim] and the six Kronecker
@@ -678,6 +717,13 @@ __global__ void __launch_bounds__(256) slot_hadamard_mlp_kernel(KtMlpArgs a) {
     const float *__restrict__ d3 = a.w[3], *__restrict__ d4 = a.w[4], *__restrict__ cond_v = a.w[11];
     const float *__restrict__ cond_u = a.w[12], *__restrict__ pre = a.pre_norm;
     const int32_t *__restrict__ perm_a = a.perm_a, *__restrict__ perm_b = a.perm_b;
+    // the Kronecker products four columns a thread where the shared arrays sit on 16-byte boundaries
+    const bool quads = dim % 4 == 0 && rows % 4 == 0 && cols % 4 == 0 && input_rows % 4 == 0;
+    auto kron = [&](const float *z, int active, const float *l, const float *r, int rw, int cl, int res_rows,
+                    float *t, float *out) {
+        if (quads) mlp_kron4(z, active, l, r, rw, cl, res_rows, t, out);
+        else mlp_kron(z, active, l, r, rw, cl, res_rows, t, out);
+    };
     if (a.pn_x) {
         // Scalar.PostNormAdd first: the projection's squares summed in order, then
         // residual + gate ((1 + scale) x) inverse, kept in res
@@ -766,7 +812,7 @@ __global__ void __launch_bounds__(256) slot_hadamard_mlp_kernel(KtMlpArgs a) {
     mlp_batched<4>(input_rows * cols, tid, nt, [&](int i) { return i < dim ? __ldg(d1 + i) : 0.0f; },
                    [&](int i, float w) { front[i] = i < dim ? __fmul_rn(normalized[i], w) : 0.0f; });
     __syncthreads();
-    mlp_kron(front, input_rows, left1, right1, rows, cols, rows, tmp, back);
+    kron(front, input_rows, left1, right1, rows, cols, rows, tmp, back);
     mlp_batched<4>(width, tid, nt,
                    [&](int n) {
                        MlpCondition c;
@@ -785,11 +831,11 @@ __global__ void __launch_bounds__(256) slot_hadamard_mlp_kernel(KtMlpArgs a) {
                        front[n] = __fmul_rn(v, sigmoid_rn(v));
                    });
     __syncthreads();
-    mlp_kron(front, rows, left2, right2, rows, cols, rows, tmp, back);
+    kron(front, rows, left2, right2, rows, cols, rows, tmp, back);
     mlp_batched<4>(width, tid, nt, [&](int n) { return make_float2(__int_as_float(__ldg(perm_b + n)), __ldg(d3 + n)); },
                    [&](int n, float2 p) { front[n] = __fmul_rn(back[__float_as_int(p.x)], p.y); });
     __syncthreads();
-    mlp_kron(front, rows, left3, right3, rows, cols, output_rows, tmp, back);
+    kron(front, rows, left3, right3, rows, cols, output_rows, tmp, back);
     mlp_batched<4>(dim, tid, nt, [&](int i) { return __ldg(d4 + i); }, [&](int i, float w) {
         const float r = __fadd_rn(res[i], __fmul_rn(a.scale, __fmul_rn(back[i], w)));
         residual[i] = r;
