@@ -80,6 +80,7 @@ struct N3State {
     // step buffers
     int32_t *d_rows = nullptr;  // tokens, slots, heads [max_rows] each
     int32_t *h_rows = nullptr;  // pinned staging
+    cudaEvent_t rows_copied = nullptr;  // the last forward's staging copy (h_rows is free once it has run)
     float *gathered, *stream, *next, *u, *residual, *norm4, *pre, *post, *res, *hpre, *post_gate, *mix_logits, *mix;
     const int32_t *perm_a = nullptr, *perm_b = nullptr;  // the model's HadamardMlp permutations (device)
     int hada_rows = 0, hada_cols = 0;
@@ -630,7 +631,9 @@ int n3_forward(N3State *s, cudaStream_t st, const int *tokens, const int *row_sl
     }
     for (int h = 0; h < heads; h++)
         if (head_rows[h] < 0 || head_rows[h] >= rows) return set_error(NDL_ERR_INVALID_ARG, "head row %d", head_rows[h]);
-    // staging: per wave its tokens, then its slots, then its head rows (indices within the wave)
+    // staging: per wave its tokens, then its slots, then its head rows (indices within the wave); the
+    // previous forward's copy out of h_rows must have run before it is rewritten
+    NDL_CUDA(cudaEventSynchronize(s->rows_copied));
     int32_t *h = s->h_rows;
     std::vector<int> start(waves + 1, 0), hstart(waves + 1, 0), head_dst;
     int at = 0;
@@ -656,12 +659,14 @@ int n3_forward(N3State *s, cudaStream_t st, const int *tokens, const int *row_sl
     }
     hstart[waves] = hat;
     NDL_CUDA(cudaMemcpyAsync(s->d_rows, h, (size_t)(2 * rows + heads) * sizeof(int32_t), cudaMemcpyHostToDevice, st));
+    NDL_CUDA(cudaEventRecord(s->rows_copied, st));
     bool in_order = waves == 1;
     for (int k = 0; k < heads && in_order; k++) in_order = head_dst[k] == k;
-    if (in_order) {  // a decode step: one wave, the logits straight into place, from a captured graph
+    if (in_order) {
+        // a decode step: one wave, the logits straight into place, from a captured graph; the call returns
+        // without waiting, so forwards of several engines run side by side
         N3_TRY(launch_wave_graph(s, rows, heads, logits, st));
         for (int r = 0; r < rows; r++) s->host_len[row_slots[r]]++;
-        NDL_CUDA(cudaStreamSynchronize(st));
         return NDL_OK;
     }
     for (int w = 0; w < waves; w++) {
@@ -951,6 +956,10 @@ int n3_create(const ndl_model *m, int slots, int capacity, int max_rows, int max
         if (ndl_model_get_tensor(m, "probe.probe_vectors", info.confidence_head, &pv) == NDL_OK && L + 1 > 0)
             s->pool_rows = (pv.rows / (L + 1)) * (L + 1);
     }
+    if (cudaEventCreateWithFlags(&s->rows_copied, cudaEventDisableTiming) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(set_error(NDL_ERR_CUDA, "n3 event"));
+    }
     if (cudaMallocHost(&s->h_rows, (size_t)3 * R * sizeof(int32_t)) != cudaSuccess)
         return fail(set_error(NDL_ERR_OUT_OF_MEMORY, "Needle-3 staging"));
     s->engram_ws_bytes = s->sites > 0 ? ndl_engram_workspace(m, R) : 0;
@@ -986,6 +995,7 @@ void n3_destroy(N3State *s) {
     for (auto &g : s->graphs) cudaGraphExecDestroy(g.exec);
     for (void *p : s->allocations) cudaFree(p);
     if (s->h_rows) cudaFreeHost(s->h_rows);
+    if (s->rows_copied) cudaEventDestroy(s->rows_copied);
     delete s;
 }
 
