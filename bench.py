@@ -1216,12 +1216,19 @@ def whistle_cpu_sample(a, seconds=5.0):
                       f"(oracle/whistle.py), 1 thread; {host_cpu()[0]}"}
 
 
+WHISTLE_UTTERANCES = 8  # clips encoded side by side per GPU, each on its own encoder and stream
+
+
 def run_whistle(args, rank, world, local):
     """Row f4: Whistle.Encode + BuildCrossMemory through ndl_whistle_* on a synthetic archive of the speech
-    model's shape, a 20 s clip per step (the reference's published Whistle figure is for a 20 s clip).
-    value = audio seconds encoded per second of device time (CUDA events on the encoder's stream around the
-    timed steps, PCM already on the device; max over ranks); e2e = the same through ndl_whistle_encode with
-    the PCM copied from pinned host memory and the encoder output read back every step."""
+    model's shape.  A step encodes 8 different 20 s clips (the reference's published Whistle figure is for a
+    20 s clip), each on its own encoder and stream over the one loaded model: every clip's encode is queued
+    (ndl_whistle_encode_device), then all are waited for.  value = audio seconds encoded per second of
+    device time (CUDA events around the timed steps, every stream joined, PCM already on the device; max
+    over ranks); e2e = the same with the PCM of every clip queued from pinned host memory and every encoder
+    output read back (ndl_whistle_read) each step."""
+    import ctypes
+
     import torch
 
     pkg = entry.load_package()
@@ -1232,66 +1239,77 @@ def run_whistle(args, rank, world, local):
     wmod = __import__("needle_cs_b200.whistle", fromlist=["whistle"])
     sys.path.insert(0, os.path.join(ROOT, "tests"))
     from whistle_support import speech_like
+    from needle_cs_b200._native import call
 
     a = whistle_bench_archive(seed=5)
     m = cact.Model(a.build(), device=local)
-    w = wmod.Whistle(m, max_seconds=WHISTLE_SECONDS)
-    pcm_host = torch.from_numpy(speech_like(WHISTLE_SECONDS, seed=rank)).pin_memory()
-    pcm_dev = pcm_host.to(device)
-    n = pcm_host.numel()
-    from needle_cs_b200._native import call
+    U = WHISTLE_UTTERANCES
+    encoders = [wmod.Whistle(m, max_seconds=WHISTLE_SECONDS) for _ in range(U)]
+    pcm_host = [torch.from_numpy(speech_like(WHISTLE_SECONDS, seed=rank * U + u)).pin_memory() for u in range(U)]
+    pcm_dev = [p.to(device) for p in pcm_host]
+    n = pcm_host[0].numel()
+
+    def step(pcms):
+        for w, p in zip(encoders, pcms):
+            call("ndl_whistle_encode_device", w._h, p.data_ptr(), n)
 
     for _ in range(args.warmup):
-        call("ndl_whistle_encode_device", w._h, pcm_dev.data_ptr(), n)
+        step(pcm_dev)
     torch.cuda.synchronize()
-    stream = torch.cuda.ExternalStream(w.stream())
+    streams = [torch.cuda.ExternalStream(w.stream()) for w in encoders]
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier(world)
     with ClockSampler(torch.cuda.get_device_properties(device).uuid) as clocks:
-        e0.record(stream)
+        e0.record(streams[0])
+        for st in streams[1:]:
+            st.wait_event(e0)
         for _ in range(args.steps):
-            call("ndl_whistle_encode_device", w._h, pcm_dev.data_ptr(), n)
-        e1.record(stream)
+            step(pcm_dev)
+        for st in streams[1:]:
+            done = torch.cuda.Event()
+            done.record(st)
+            streams[0].wait_event(done)
+        e1.record(streams[0])
         torch.cuda.synchronize()
     ms = max_over_ranks(e0.elapsed_time(e1), world)
-    import ctypes
-
     fr = ctypes.c_int()
-    call("ndl_whistle_frames", w._h, ctypes.byref(fr), None)
+    call("ndl_whistle_frames", encoders[0]._h, ctypes.byref(fr), None)
     frames = fr.value
-    out = np.empty((frames, m.info["dim"]), np.float32)
+    outs = [np.empty((frames, m.info["dim"]), np.float32) for _ in range(U)]
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        w.encode(pcm_host.numpy())
-        out = w.encoder_output()
+        step(pcm_host)
+        for w, o in zip(encoders, outs):
+            call("ndl_whistle_read", w._h, 2, 0, o.ctypes.data, o.nbytes, None)
     wall = max_over_ranks((time.perf_counter() - t0) * 1e3, world)
-    value = world * WHISTLE_SECONDS * args.steps / (ms * 1e-3)
-    E, L, d = WHISTLE_AUDIO["encoder_layers"], WHISTLE_SHAPE["layers"], WHISTLE_SHAPE["dim"]
+    value = world * U * WHISTLE_SECONDS * args.steps / (ms * 1e-3)
+    E, L = WHISTLE_AUDIO["encoder_layers"], WHISTLE_SHAPE["layers"]
     weights = sum(len(r[4]) for r in a.records if r[0] == "audio")
-    achieved = weights / (ms * 1e-3 / args.steps) / 1e9
+    achieved = U * weights / (ms * 1e-3 / args.steps) / 1e9
     peak, peak_source = hbm_peak()
     line = {"metric": "whistle encode audio seconds/sec/box", "value": value, "unit": "audio s/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32 front end, u2/u4 codes x int8 -> int32, f32",
             "data": "synthetic",
             "config": {"workload": "whistle_encode", "model": "synthetic archive of the Whistle speech model's shape",
-                       "clip_seconds": WHISTLE_SECONDS, "frames": frames, "geometry": dict(WHISTLE_SHAPE),
-                       "audio": dict(WHISTLE_AUDIO), "weight_bytes": weights,
-                       "l2": "weights fit L2; each step reads them once per layer pass"},
-            "roofline": {"bound": "hbm", "kernel": "the whole encode (latency-bound chain of small kernels)",
+                       "clip_seconds": WHISTLE_SECONDS, "clips_per_step": U, "frames": frames,
+                       "geometry": dict(WHISTLE_SHAPE), "audio": dict(WHISTLE_AUDIO), "weight_bytes": weights,
+                       "l2": "weights fit L2; each clip reads them once per layer pass"},
+            "roofline": {"bound": "hbm", "kernel": "the whole encode (latency-bound chains of small kernels)",
                          "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                         "traffic": None, "peak_source": peak_source, "algorithmic_bytes_per_step": weights},
-            "e2e": {"value": world * WHISTLE_SECONDS * args.steps / (wall * 1e-3), "unit": "audio s/s",
-                    "h2d_bytes_per_step": n * 4, "d2h_bytes_per_step": out.nbytes},
+                         "traffic": None, "peak_source": peak_source, "algorithmic_bytes_per_step": U * weights},
+            "e2e": {"value": world * U * WHISTLE_SECONDS * args.steps / (wall * 1e-3), "unit": "audio s/s",
+                    "h2d_bytes_per_step": U * n * 4, "d2h_bytes_per_step": sum(o.nbytes for o in outs)},
             # per encode: front end 4, stem 11, lanes + fill 2, 20 a layer, final 2, cross rows and Prepare 2,
             # 2 per decoder layer
-            "gpu_launches": args.steps * (4 + 11 + 2 + 20 * E + 2 + 2 + 2 * L), "clocks": clocks.summary()}
+            "gpu_launches": args.steps * U * (4 + 11 + 2 + 20 * E + 2 + 2 + 2 * L), "clocks": clocks.summary()}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         entry.load_oracle()
         line["cpu_baseline"] = whistle_cpu_sample(a)
     if rank == 0:
         print(json.dumps(line), flush=True)
-    w.close()
+    for w in encoders:
+        w.close()
     m.close()
 
 
