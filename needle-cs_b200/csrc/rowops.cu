@@ -596,7 +596,9 @@ __device__ void mlp_kron(const float *z, int active_rows, const float *left, con
 // mlp_kron with each thread on four adjacent columns of one output row
 // (cols % 4 == 0, every array on 16-byte boundaries): per step one broadcast
 // load of the left (or tmp) value and one 16-byte load of z (or right) feed
-// four chains, the same products and sums in the same order.
+// four chains, the same products and sums in the same order.  tmp rows are
+// cols + 4 floats apart, so the four rows a warp reads in the second product
+// sit in four different banks (at a stride of cols they would share one).
 __device__ void mlp_kron4(const float *z, int active_rows, const float *left, const float *right, int rows, int cols,
                           int result_rows, float *tmp, float *result) {
     const int quads = cols >> 2, n = result_rows * quads;
@@ -612,7 +614,7 @@ __device__ void mlp_kron4(const float *z, int active_rows, const float *left, co
             acc.z = __fadd_rn(acc.z, __fmul_rn(l, zz.z));
             acc.w = __fadd_rn(acc.w, __fmul_rn(l, zz.w));
         }
-        *reinterpret_cast<float4 *>(tmp + k * cols + c) = acc;
+        *reinterpret_cast<float4 *>(tmp + k * (cols + 4) + c) = acc;
     }
     __syncthreads();
     for (int u = threadIdx.x; u < n; u += blockDim.x) {
@@ -620,7 +622,7 @@ __device__ void mlp_kron4(const float *z, int active_rows, const float *left, co
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll 4
         for (int j = 0; j < cols; j++) {
-            const float t = tmp[k * cols + j];
+            const float t = tmp[k * (cols + 4) + j];
             const float4 rr = *reinterpret_cast<const float4 *>(right + j * cols + c);
             acc.x = __fadd_rn(acc.x, __fmul_rn(t, rr.x));
             acc.y = __fadd_rn(acc.y, __fmul_rn(t, rr.y));
@@ -633,14 +635,15 @@ __device__ void mlp_kron4(const float *z, int active_rows, const float *left, co
 }
 
 // Shared floats of slot_hadamard_mlp_kernel: weights[8], normalized[dim],
-// front / back / tmp [width], scratch[8 * dim] (squares, then the
-// ConditionWeights products), the residual row [dim] and the six Kronecker
-// factors (the first left factor's in_rows x rows, two more rows x rows,
-// three cols x cols).
+// front / back [width], tmp [rows][cols + 4], scratch[8][dim + 4] (squares,
+// then the ConditionWeights products, rows dim + 4 apart so that the eight
+// products of one normalized element land in eight banks), the residual row
+// [dim] and the six Kronecker factors (the first left factor's in_rows x
+// rows, two more rows x rows, three cols x cols).
 __host__ __device__ inline size_t mlp_smem_floats(int dim, int rows, int cols) {
     const size_t in_rows = (size_t)(dim + cols - 1) / cols;
-    return 8 + (size_t)dim + 3 * (size_t)rows * cols + 9 * (size_t)dim + (in_rows + 2 * (size_t)rows) * rows +
-           3 * (size_t)cols * cols;
+    return 8 + (size_t)dim + 2 * (size_t)rows * cols + (size_t)rows * (cols + 4) + 8 * ((size_t)dim + 4) +
+           (size_t)dim + (in_rows + 2 * (size_t)rows) * rows + 3 * (size_t)cols * cols;
 }
 
 // Element loop over [0, n) in which every thread issues the loads of kBatch
@@ -710,7 +713,8 @@ __global__ void __launch_bounds__(256) slot_hadamard_mlp_kernel(KtMlpArgs a) {
     const int output_rows = min(rows, (input_rows + 3) / 4 * 4);
     const int tid = threadIdx.x, nt = blockDim.x;
     float *weights = sm, *normalized = sm + 8, *front = normalized + dim, *back = front + width, *tmp = back + width;
-    float *scratch = tmp + width, *res = scratch + 8 * dim;
+    const int sd = dim + 4;  // scratch row stride
+    float *scratch = tmp + rows * (cols + 4), *res = scratch + 8 * sd;
     float *left1 = res + dim, *right1 = left1 + input_rows * rows, *left2 = right1 + cols * cols;
     float *right2 = left2 + rows * rows, *left3 = right2 + cols * cols, *right3 = left3 + rows * rows;
     const float *__restrict__ d1 = a.w[0], *__restrict__ d2 = a.w[1], *__restrict__ b2 = a.w[2];
@@ -792,9 +796,9 @@ __global__ void __launch_bounds__(256) slot_hadamard_mlp_kernel(KtMlpArgs a) {
     // ConditionWeights: products in parallel (weight j's row of dim contiguous),
     // weight j summed in order by thread j
     mlp_batched<8>(dim * 8, tid, nt, [&](int e) { return __ldg(cond_v + e); },
-                   [&](int e, float w) { scratch[(e & 7) * dim + (e >> 3)] = __fmul_rn(normalized[e >> 3], w); });
+                   [&](int e, float w) { scratch[(e & 7) * sd + (e >> 3)] = __fmul_rn(normalized[e >> 3], w); });
     __syncthreads();
-    if (tid < 8) weights[tid] = mlp_ordered_sum(scratch + tid * dim, dim);
+    if (tid < 8) weights[tid] = mlp_ordered_sum(scratch + tid * sd, dim);
     __syncthreads();
     // Softmax over the 8 weights: the peak and the exponentials on 8 threads, the
     // total in order and the divisions on thread 0
