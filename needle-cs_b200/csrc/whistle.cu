@@ -247,9 +247,12 @@ __global__ void wh_standardize_kernel(float *__restrict__ x, long long n, int co
 __global__ void wh_stem1_kernel(const float *__restrict__ feats, int l0, int mels, const float *__restrict__ w, int s,
                                 int l1, float *__restrict__ out) {
     pdl_enter();
-    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= (long long)l1 * 40 * s) return;
-    const int c = (int)(i % s), f = (int)((i / s) % 40), p = (int)(i / ((long long)40 * s));
+    // 32-bit index arithmetic (a stage holds fewer than 2^31 elements, checked when the encoder is created):
+    // a 64-bit division is a long software sequence on the GPU
+    const unsigned i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (unsigned)l1 * 40u * (unsigned)s) return;
+    const unsigned pf = i / (unsigned)s;
+    const int c = (int)(i - pf * (unsigned)s), f = (int)(pf % 40u), p = (int)(pf / 40u);
     float o = 0.0f;
     for (int dt = 0; dt < 3; dt++) {
         const int r = 2 * p - 1 + dt;
@@ -270,9 +273,10 @@ __global__ void wh_depthwise_kernel(const float *__restrict__ src, int rows_in, 
                                     const float *__restrict__ w, int s, int rows_out, int freq_out,
                                     float *__restrict__ out) {
     pdl_enter();
-    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= (long long)rows_out * freq_out * s) return;
-    const int c = (int)(i % s), f = (int)((i / s) % freq_out), q = (int)(i / ((long long)freq_out * s));
+    const unsigned i = blockIdx.x * blockDim.x + threadIdx.x;  // 32-bit index arithmetic, as in wh_stem1_kernel
+    if (i >= (unsigned)rows_out * (unsigned)freq_out * (unsigned)s) return;
+    const unsigned pf = i / (unsigned)s;
+    const int c = (int)(i - pf * (unsigned)s), f = (int)(pf % (unsigned)freq_out), q = (int)(pf / (unsigned)freq_out);
     float o = 0.0f;
     for (int dt = 0; dt < 3; dt++) {
         const int r = 2 * q - 1 + dt;
@@ -297,9 +301,10 @@ __global__ void wh_silu_kernel(float *__restrict__ x, long long n) {
 // = row[r][f][c].
 __global__ void wh_silu_transpose_kernel(const float *__restrict__ src, int rows, int s, float *__restrict__ flat) {
     pdl_enter();
-    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= (long long)rows * 10 * s) return;
-    const int c = (int)(i % s), f = (int)((i / s) % 10), r = (int)(i / ((long long)10 * s));
+    const unsigned i = blockIdx.x * blockDim.x + threadIdx.x;  // 32-bit index arithmetic, as in wh_stem1_kernel
+    if (i >= (unsigned)rows * 10u * (unsigned)s) return;
+    const unsigned pf = i / (unsigned)s;
+    const int c = (int)(i - pf * (unsigned)s), f = (int)(pf % 10u), r = (int)(pf / 10u);
     const float v = src[i];
     flat[(size_t)r * 10 * s + (size_t)c * 10 + f] = __fmul_rn(v, sigmoid_rn(v));
 }
@@ -920,6 +925,10 @@ int whistle_buffers(ndl_whistle *w) {
     const size_t cols = std::max(std::max(s, 10 * s), std::max(4 * d, H * VD));
     const size_t tokens = std::max(stem_tokens, F);
     w->act_stride = (int)((cols / 128 + 7) & ~(size_t)7);
+    // the stem kernels index their stages in 32 bits; the first stage is the largest
+    if ((size_t)w->max_l1 * 40 * s >= ((size_t)1 << 31))
+        return set_error(NDL_ERR_UNSUPPORTED, "whistle: %d samples at stem width %zu exceed the stem's 2^31 elements",
+                         w->max_samples, s);
     WH_TRY(whistle_buf(w, &w->peak, 1));
     WH_TRY(whistle_buf(w, &w->status, 1));
     WH_TRY(whistle_buf(w, &w->padded, (size_t)w->window + w->max_samples + w->hop + w->fft));
