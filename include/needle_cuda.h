@@ -794,7 +794,9 @@ NDL_API int ndl_model_tokenizer(const ndl_model *m, const void **blob, size_t *b
  *   _VALUES int8 [frames][heads][v], _VALUE_SCALES fp32 [frames][heads].
  * NDL_ERR_UNSUPPORTED for an archive without audio or a geometry the device
  * encoder does not take (CQ widths not in 128-column groups, dim > 1024,
- * head dims > 64, more than 128 mels, fft > 4096 or not a power of two). */
+ * head dims > 64, more than 128 mels, fft > 4096 or not a power of two), or a
+ * max_samples whose first stem stage (half the mel frames x 40 x the stem
+ * width) would hold 2^31 elements or more. */
 typedef struct ndl_whistle ndl_whistle;
 enum {
     NDL_WHISTLE_MEL = 0,
