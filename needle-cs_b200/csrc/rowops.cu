@@ -898,7 +898,7 @@ int launch_slot_hadamard_mlp(const KtMlpArgs &a, cudaStream_t stream) {
     const size_t smem = mlp_smem_floats(a.dim, a.rows, a.cols) * 4;
     if (smem > 200 * 1024) return set_error(NDL_ERR_UNSUPPORTED, "hadamard_mlp: dim %d x width %d too large", a.dim,
                                             a.rows * a.cols);
-    cudaFuncSetAttribute(slot_hadamard_mlp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    NDL_CUDA(cudaFuncSetAttribute(slot_hadamard_mlp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     slot_hadamard_mlp_kernel<<<1, 256, smem, stream>>>(a);
     return check_launch("slot_hadamard_mlp");
 }
